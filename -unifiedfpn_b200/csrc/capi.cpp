@@ -1,0 +1,602 @@
+// extern "C" boundary of libunified_fpn_b200.so (declared in include/unified_fpn_c.h).
+// Every entry point catches exceptions, stores a message for ufpn_last_error()
+// and returns a status code; nothing here calls exit().
+#include <cuda_runtime.h>
+
+#include <chrono>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <map>
+#include <mutex>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "kernels.h"
+#include "unified_fpn/core/engine.h"
+#include "unified_fpn_c.h"
+
+using ufpn::DType;
+using ufpn::Layout;
+
+struct ufpn_core {
+  UnifiedFPNCore core;
+  ufpn_core(int dev, size_t ws) : core(ws, dev) {}
+};
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(UFPN_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+bool parse_dtype(int code, DType* out) {
+  switch (code) {
+    case UFPN_DTYPE_F32:
+      *out = DType::F32;
+      return true;
+    case UFPN_DTYPE_F16:
+      *out = DType::F16;
+      return true;
+    case UFPN_DTYPE_BF16:
+      *out = DType::BF16;
+      return true;
+    default:
+      return false;
+  }
+}
+bool parse_layout(int code, Layout* out) {
+  if (code == UFPN_LAYOUT_NCHW) {
+    *out = Layout::NCHW;
+    return true;
+  }
+  if (code == UFPN_LAYOUT_NHWC) {
+    *out = Layout::NHWC;
+    return true;
+  }
+  return false;
+}
+
+// One lazily allocated status word per device for the standalone tensor-core entry points.
+std::mutex g_status_mu;
+int* g_status[64] = {};
+int* device_status_word() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(g_status_mu);
+  if (!g_status[dev]) {
+    int* p = nullptr;
+    if (cudaMalloc(&p, 256) != cudaSuccess) return nullptr;
+    cudaMemset(p, 0, 256);
+    g_status[dev] = p;
+  }
+  return g_status[dev];
+}
+
+template <typename F>
+int guarded(F&& f) {
+  try {
+    return f();
+  } catch (const std::exception& e) {
+    return fail(UFPN_ERR_STATE, e.what());
+  } catch (...) {
+    return fail(UFPN_ERR_STATE, "unknown C++ exception");
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ufpn_last_error(void) { return g_last_error.c_str(); }
+
+int ufpn_version(void) { return 100; }
+
+int ufpn_device_status(int reset, int* status_out) {
+  int* w = device_status_word();
+  if (!w) return fail(UFPN_ERR_CUDA, "could not allocate the device status word");
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  int v = 0;
+  e = cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy");
+  if (reset) cudaMemset(w, 0, sizeof(int));
+  if (status_out) *status_out = v;
+  return UFPN_OK;
+}
+
+// ------------------------------------------------------------------ engine
+int ufpn_core_create(int device, size_t workspace_bytes, ufpn_core** out) {
+  if (!out) return fail(UFPN_ERR_INVALID_ARG, "out is NULL");
+  *out = nullptr;
+  return guarded([&] {
+    *out = new ufpn_core(device, workspace_bytes);
+    return UFPN_OK;
+  });
+}
+
+void ufpn_core_destroy(ufpn_core* core) { delete core; }
+
+int ufpn_core_configure_levels(ufpn_core* core, int batch, const int* in_channels,
+                               const int* heights, const int* widths, int output_channels,
+                               int dtype, int layout) {
+  if (!core || !in_channels || !heights || !widths) return fail(UFPN_ERR_INVALID_ARG, "NULL");
+  DType dt;
+  Layout lay;
+  if (!parse_dtype(dtype, &dt)) return fail(UFPN_ERR_UNSUPPORTED, "unsupported dtype");
+  if (!parse_layout(layout, &lay)) return fail(UFPN_ERR_INVALID_ARG, "bad layout");
+  return guarded([&] {
+    std::vector<FPNDimensions> dims(4);
+    for (int l = 0; l < 4; ++l) dims[l] = {batch, in_channels[l], heights[l], widths[l], 0};
+    core->core.configure_levels(dims, output_channels, static_cast<FPNDataType>(dtype),
+                                lay == Layout::NHWC ? FPNLayout::NHWC : FPNLayout::NCHW);
+    return UFPN_OK;
+  });
+}
+
+int ufpn_core_set_weights(ufpn_core* core, int level, const float* lateral_w,
+                          const float* lateral_b, const float* output_w, const float* output_b) {
+  if (!core) return fail(UFPN_ERR_INVALID_ARG, "NULL core");
+  return guarded([&] {
+    core->core.set_weights(level, lateral_w, lateral_b, output_w, output_b);
+    return UFPN_OK;
+  });
+}
+
+int ufpn_core_allocate_weights(ufpn_core* core, const int* in_channels, int output_channels) {
+  if (!core || !in_channels) return fail(UFPN_ERR_INVALID_ARG, "NULL");
+  return guarded([&] {
+    core->core.allocate_weights(std::vector<int>(in_channels, in_channels + 4), output_channels);
+    return UFPN_OK;
+  });
+}
+
+int ufpn_core_forward(ufpn_core* core, const void* const* inputs, void* const* outputs, void* p6,
+                      void* stream) {
+  if (!core || !inputs || !outputs) return fail(UFPN_ERR_INVALID_ARG, "NULL");
+  return guarded([&] {
+    core->core.forward_raw(inputs, outputs, p6, static_cast<cudaStream_t>(stream));
+    return UFPN_OK;
+  });
+}
+
+int ufpn_core_set_kernel_config(ufpn_core* core, int tile_size, int channels_per_thread,
+                                int use_tensor_cores, int activation, int enable_graph_capture) {
+  if (!core) return fail(UFPN_ERR_INVALID_ARG, "NULL core");
+  return guarded([&] {
+    FPNKernelConfig c;
+    c.tile_size = tile_size;
+    c.channels_per_thread = channels_per_thread;
+    c.use_tensor_cores = use_tensor_cores != 0;
+    c.activation = static_cast<FPNActivation>(activation);
+    c.enable_graph_capture = enable_graph_capture != 0;
+    core->core.set_kernel_config(c);
+    return UFPN_OK;
+  });
+}
+
+size_t ufpn_core_get_memory_usage(const ufpn_core* core) {
+  return core ? core->core.get_memory_usage() : 0;
+}
+
+int ufpn_core_get_performance_metrics(const ufpn_core* core, float* kernel_times_ms,
+                                      float* metrics) {
+  if (!core) return fail(UFPN_ERR_INVALID_ARG, "NULL core");
+  const FPNPerformanceMetrics& m = core->core.get_performance_metrics();
+  if (kernel_times_ms) std::memcpy(kernel_times_ms, m.kernel_times_ms, sizeof(m.kernel_times_ms));
+  if (metrics) {
+    metrics[0] = m.forward_time_ms;
+    metrics[1] = m.memory_bandwidth_gb_s;
+    metrics[2] = m.compute_utilization;
+    metrics[3] = static_cast<float>(m.peak_memory_usage_bytes) / (1024.f * 1024.f);
+    metrics[4] = static_cast<float>(m.num_kernel_launches);
+  }
+  return UFPN_OK;
+}
+
+int ufpn_core_set_profiling(ufpn_core* core, int enable) {
+  if (!core) return fail(UFPN_ERR_INVALID_ARG, "NULL core");
+  core->core.set_profiling(enable != 0);
+  return UFPN_OK;
+}
+
+int ufpn_core_autotune(ufpn_core* core, const void* const* inputs, void* const* outputs,
+                       void* p6, void* stream, int iterations) {
+  if (!core || !inputs || !outputs) return fail(UFPN_ERR_INVALID_ARG, "NULL");
+  return guarded([&] {
+    g_last_error = core->core.autotune(inputs, outputs, p6, static_cast<cudaStream_t>(stream),
+                                       iterations);
+    return UFPN_OK;
+  });
+}
+
+int ufpn_core_save_tuning(const ufpn_core* core, const char* path) {
+  if (!core || !path) return fail(UFPN_ERR_INVALID_ARG, "NULL");
+  return core->core.save_tuning(path) ? UFPN_OK : fail(UFPN_ERR_STATE, "cannot write file");
+}
+
+int ufpn_core_load_tuning(ufpn_core* core, const char* path) {
+  if (!core || !path) return fail(UFPN_ERR_INVALID_ARG, "NULL");
+  return core->core.load_tuning(path) ? UFPN_OK : fail(UFPN_ERR_STATE, "cannot read file");
+}
+
+int ufpn_core_device_status(ufpn_core* core, int reset, int* status_out) {
+  if (!core) return fail(UFPN_ERR_INVALID_ARG, "NULL core");
+  return guarded([&] {
+    const int v = core->core.device_status(reset != 0);
+    if (status_out) *status_out = v;
+    return UFPN_OK;
+  });
+}
+
+// ------------------------------------------------------------------ standalone ops
+int ufpn_lateral_conv(int dtype, int layout, const void* x, const void* w, const float* bias,
+                      const void* coarse, void* out, int N, int Cin, int H, int W, int Cout,
+                      int Hc, int Wc, void* stream) {
+  DType dt;
+  Layout lay;
+  if (!parse_dtype(dtype, &dt)) return fail(UFPN_ERR_UNSUPPORTED, "unsupported dtype");
+  if (!parse_layout(layout, &lay)) return fail(UFPN_ERR_INVALID_ARG, "bad layout");
+  if (!x || !w || !bias || !out) return fail(UFPN_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (N <= 0 || Cin <= 0 || H <= 0 || W <= 0 || Cout <= 0)
+    return fail(UFPN_ERR_INVALID_ARG, "sizes must be positive");
+  if (coarse && (Hc <= 0 || Wc <= 0 || Hc > H || Wc > W))
+    return fail(UFPN_ERR_INVALID_ARG, "coarse map must be non-empty and not larger than output");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dt == DType::F32) {
+    if (lay != Layout::NCHW) return fail(UFPN_ERR_UNSUPPORTED, "fp32 lateral takes NCHW");
+    cudaError_t e = ufpn::launch_fp32_lateral(
+        static_cast<const float*>(x), static_cast<const float*>(w), bias,
+        static_cast<const float*>(coarse), static_cast<float*>(out), N, Cin, Cout, H, W,
+        coarse ? Hc : 1, coarse ? Wc : 1, s);
+    return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "fp32 lateral");
+  }
+  if (lay != Layout::NHWC) return fail(UFPN_ERR_UNSUPPORTED, "16-bit lateral takes NHWC");
+  if (Cout != 256) return fail(UFPN_ERR_UNSUPPORTED, "the tensor-core lateral needs Cout = 256");
+  if (Cin % 8 != 0) return fail(UFPN_ERR_UNSUPPORTED, "Cin must be a multiple of 8");
+  if (!ufpn::aligned16(x) || !ufpn::aligned16(w) || !ufpn::aligned16(out) ||
+      !ufpn::aligned16(bias) || (coarse && !ufpn::aligned16(coarse)))
+    return fail(UFPN_ERR_ALIGNMENT, "tensors must be 16-byte aligned");
+  int* status = device_status_word();
+  ufpn::TcPlan plan;
+  cudaError_t e = ufpn::plan_tc_lateral(plan, dt, x, w, bias, coarse, out, N, Cin, H, W,
+                                        coarse ? Hc : 0, coarse ? Wc : 0, status, 0);
+  if (e != cudaSuccess) return cuda_fail(e, "plan lateral");
+  e = ufpn::launch_tc(plan, s);
+  return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "lateral launch");
+}
+
+int ufpn_conv3x3(int dtype, const void* x, const void* w, const float* bias, void* out, void* p6,
+                 int N, int H, int W, int tile_w, void* stream) {
+  DType dt;
+  if (!parse_dtype(dtype, &dt)) return fail(UFPN_ERR_UNSUPPORTED, "unsupported dtype");
+  if (!x || !w || !bias || !out) return fail(UFPN_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (N <= 0 || H <= 0 || W <= 0) return fail(UFPN_ERR_INVALID_ARG, "sizes must be positive");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dt == DType::F32) {
+    cudaError_t e = ufpn::launch_fp32_conv3x3(static_cast<const float*>(x),
+                                              static_cast<const float*>(w), bias,
+                                              static_cast<float*>(out), N, 256, 256, H, W, s);
+    if (e == cudaSuccess && p6)
+      e = ufpn::launch_p6(DType::F32, out, p6, N, 256, H, W, Layout::NCHW, s);
+    return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "fp32 conv3x3");
+  }
+  if (!ufpn::aligned16(x) || !ufpn::aligned16(w) || !ufpn::aligned16(out) ||
+      !ufpn::aligned16(bias) || (p6 && !ufpn::aligned16(p6)))
+    return fail(UFPN_ERR_ALIGNMENT, "tensors must be 16-byte aligned");
+  ufpn::Conv3x3Tiling t;
+  if (tile_w > 0) {
+    if (tile_w > 128 || 128 % tile_w != 0)
+      return fail(UFPN_ERR_INVALID_ARG, "tile_w must be 8, 16, 32, 64 or 128");
+    t.tile_w = tile_w;
+    t.tile_h = 128 / tile_w;
+  } else {
+    long long best = -1;
+    for (int tw : {16, 8, 32, 64, 128}) {
+      const int th = 128 / tw;
+      const long long a = static_cast<long long>((W + tw - 1) / tw) * tw * ((H + th - 1) / th) * th;
+      if (best < 0 || a < best) {
+        best = a;
+        t.tile_w = tw;
+        t.tile_h = th;
+      }
+    }
+  }
+  int* status = device_status_word();
+  ufpn::TcPlan plan;
+  cudaError_t e = ufpn::plan_tc_conv3x3(plan, dt, x, w, bias, out, p6, N, H, W, t, status, 0);
+  if (e != cudaSuccess) return cuda_fail(e, "plan conv3x3");
+  e = ufpn::launch_tc(plan, s);
+  return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "conv3x3 launch");
+}
+
+int ufpn_upsample_add(int dtype, int layout, const void* coarse, const void* lateral, void* out,
+                      int N, int C, int Hc, int Wc, int H, int W, int align_corners,
+                      void* stream) {
+  DType dt;
+  Layout lay;
+  if (!parse_dtype(dtype, &dt)) return fail(UFPN_ERR_UNSUPPORTED, "unsupported dtype");
+  if (!parse_layout(layout, &lay)) return fail(UFPN_ERR_INVALID_ARG, "bad layout");
+  if (!coarse || !out) return fail(UFPN_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (N <= 0 || C <= 0 || Hc <= 0 || Wc <= 0 || H <= 0 || W <= 0)
+    return fail(UFPN_ERR_INVALID_ARG, "sizes must be positive");
+  cudaError_t e = ufpn::launch_upsample_add(dt, coarse, lateral, out, N, C, Hc, Wc, H, W,
+                                            align_corners, lay, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "upsample_add");
+}
+
+int ufpn_p6_maxpool(int dtype, int layout, const void* p5, void* p6, int N, int C, int H, int W,
+                    void* stream) {
+  DType dt;
+  Layout lay;
+  if (!parse_dtype(dtype, &dt)) return fail(UFPN_ERR_UNSUPPORTED, "unsupported dtype");
+  if (!parse_layout(layout, &lay)) return fail(UFPN_ERR_INVALID_ARG, "bad layout");
+  if (!p5 || !p6) return fail(UFPN_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (N <= 0 || C <= 0 || H <= 0 || W <= 0)
+    return fail(UFPN_ERR_INVALID_ARG, "sizes must be positive");
+  cudaError_t e = ufpn::launch_p6(dt, p5, p6, N, C, H, W, lay, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "p6");
+}
+
+int ufpn_pack_conv3x3_weights(int dtype, const float* w, void* out, int Cout, int Cin,
+                              void* stream) {
+  DType dt;
+  if (!parse_dtype(dtype, &dt) || dt == DType::F32)
+    return fail(UFPN_ERR_UNSUPPORTED, "packing targets F16 or BF16");
+  if (!w || !out || Cout <= 0 || Cin <= 0) return fail(UFPN_ERR_INVALID_ARG, "bad arguments");
+  cudaError_t e =
+      ufpn::launch_pack_conv3x3(dt, w, out, Cout, Cin, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "pack");
+}
+
+int ufpn_convert_weights(int dtype, const float* w, void* out, long long count, void* stream) {
+  DType dt;
+  if (!parse_dtype(dtype, &dt)) return fail(UFPN_ERR_UNSUPPORTED, "unsupported dtype");
+  if (!w || !out || count <= 0) return fail(UFPN_ERR_INVALID_ARG, "bad arguments");
+  cudaError_t e =
+      ufpn::launch_convert_weights(dt, w, out, count, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "convert");
+}
+
+int ufpn_layout_convert(int dtype, const void* in, void* out, int N, int C, int H, int W,
+                        int to_nhwc, void* stream) {
+  DType dt;
+  if (!parse_dtype(dtype, &dt)) return fail(UFPN_ERR_UNSUPPORTED, "unsupported dtype");
+  if (!in || !out || N <= 0 || C <= 0 || H <= 0 || W <= 0)
+    return fail(UFPN_ERR_INVALID_ARG, "bad arguments");
+  cudaError_t e = ufpn::launch_transpose(dt, in, out, N, C, H * W, to_nhwc != 0,
+                                         static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "layout convert");
+}
+
+// ------------------------------------------------------------------ reference C ABI
+namespace {
+
+// Times one upsample launch on the legacy stream with events and synchronises,
+// as the reference's launchers did (fast_upsample_kernels.cu:482-496).
+cudaError_t timed_upsample(DType dt, const void* in, void* out, int N, int C, int Hi, int Wi,
+                           int Ho, int Wo, int ac, float* ms_out, float* gbs_out) {
+  if (!in || !out || N <= 0 || C <= 0 || Hi <= 0 || Wi <= 0 || Ho <= 0 || Wo <= 0)
+    return cudaErrorInvalidValue;
+  cudaEvent_t a, b;
+  cudaEventCreate(&a);
+  cudaEventCreate(&b);
+  cudaEventRecord(a, 0);
+  cudaError_t e = ufpn::launch_upsample_add(dt, in, nullptr, out, N, C, Hi, Wi, Ho, Wo, ac,
+                                            Layout::NHWC, 0);
+  cudaEventRecord(b, 0);
+  if (e == cudaSuccess) e = cudaEventSynchronize(b);
+  float ms = 0.f;
+  if (e == cudaSuccess) cudaEventElapsedTime(&ms, a, b);
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  if (ms_out) *ms_out = ms;
+  if (gbs_out) {
+    const double bytes = static_cast<double>(N) * C * (static_cast<double>(Hi) * Wi +
+                                                        static_cast<double>(Ho) * Wo) *
+                         ufpn::dtype_size(dt);
+    *gbs_out = ms > 0 ? static_cast<float>(bytes / (ms * 1e-3) / 1e9) : 0.f;
+  }
+  return e;
+}
+
+struct UpsampleEngine {
+  int device = 0;
+  struct Rec {
+    std::string name;
+    float ms, gbs;
+    size_t bytes;
+  };
+  std::vector<Rec> recs;
+};
+
+}  // namespace
+
+cudaError_t launch_production_upsample_float(const float* input, float* output, int batch_size,
+                                             int channels, int in_height, int in_width,
+                                             int out_height, int out_width, int align_corners,
+                                             float* kernel_time_ms, float* bandwidth_gb_s) {
+  return timed_upsample(DType::F32, input, output, batch_size, channels, in_height, in_width,
+                        out_height, out_width, align_corners, kernel_time_ms, bandwidth_gb_s);
+}
+
+cudaError_t launch_production_upsample_half(const void* input, void* output, int batch_size,
+                                            int channels, int in_height, int in_width,
+                                            int out_height, int out_width, int align_corners,
+                                            float* kernel_time_ms, float* bandwidth_gb_s) {
+  return timed_upsample(DType::F16, input, output, batch_size, channels, in_height, in_width,
+                        out_height, out_width, align_corners, kernel_time_ms, bandwidth_gb_s);
+}
+
+cudaError_t launch_production_upsample_bfloat16(const void* input, void* output, int batch_size,
+                                                int channels, int in_height, int in_width,
+                                                int out_height, int out_width, int align_corners,
+                                                float* kernel_time_ms, float* bandwidth_gb_s) {
+  return timed_upsample(DType::BF16, input, output, batch_size, channels, in_height, in_width,
+                        out_height, out_width, align_corners, kernel_time_ms, bandwidth_gb_s);
+}
+
+void* create_upsample_engine(int device_id) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device_id < 0 || device_id >= n) {
+    g_last_error = "create_upsample_engine: invalid device";
+    return nullptr;
+  }
+  auto* e = new UpsampleEngine;
+  e->device = device_id;
+  return e;
+}
+
+void destroy_upsample_engine(void* engine) { delete static_cast<UpsampleEngine*>(engine); }
+
+int production_upsample_float(void* engine, const float* input, float* output, int batch_size,
+                              int channels, int in_height, int in_width, int out_height,
+                              int out_width, float scale_y, float scale_x, int align_corners,
+                              float* metrics_out) {
+  auto* eng = static_cast<UpsampleEngine*>(engine);
+  if (!eng) return -1;
+  (void)scale_y;  // the scale is derived from the sizes (in / out), as the kernels did
+  (void)scale_x;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(eng->device);
+  float ms = 0.f, gbs = 0.f;
+  cudaError_t e = timed_upsample(DType::F32, input, output, batch_size, channels, in_height,
+                                 in_width, out_height, out_width, align_corners, &ms, &gbs);
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) {
+    g_last_error = std::string("production_upsample_float: ") + cudaGetErrorString(e);
+    return -1;
+  }
+  const size_t bytes = static_cast<size_t>(batch_size) * channels *
+                       (static_cast<size_t>(in_height) * in_width +
+                        static_cast<size_t>(out_height) * out_width) * 4;
+  eng->recs.push_back({"bilinear_upsample_f32", ms, gbs, bytes});
+  if (metrics_out) {
+    metrics_out[0] = ms;
+    metrics_out[1] = gbs;
+    metrics_out[2] = 0.f;
+    metrics_out[3] = static_cast<float>(bytes);
+  }
+  return 0;
+}
+
+void print_upsample_profiling_summary(void* engine) {
+  auto* eng = static_cast<UpsampleEngine*>(engine);
+  if (!eng) return;
+  double tot = 0;
+  for (auto& r : eng->recs) tot += r.ms;
+  std::printf("upsample engine (device %d): %zu calls, %.4f ms total\n", eng->device,
+              eng->recs.size(), tot);
+  for (auto& r : eng->recs)
+    std::printf("  %-24s %9.4f ms %9.1f GB/s %12zu B\n", r.name.c_str(), r.ms, r.gbs, r.bytes);
+}
+
+int export_upsample_profiling_data(void* engine, const char* filename) {
+  auto* eng = static_cast<UpsampleEngine*>(engine);
+  if (!eng || !filename) return -1;
+  std::ofstream f(filename);
+  if (!f) return -1;
+  f << "kernel,time_ms,bandwidth_gb_s,bytes\n";
+  for (auto& r : eng->recs) f << r.name << "," << r.ms << "," << r.gbs << "," << r.bytes << "\n";
+  return f ? 0 : -1;
+}
+
+// ------------------------------------------------------------------ autotuner C ABI
+namespace {
+std::mutex g_tune_mu;
+std::map<std::tuple<int, int, int, int, int>, TuningResult> g_tune_results;
+}  // namespace
+
+TuningResult* fpn_auto_tune_lateral_conv(int batch_size, int in_channels, int out_channels,
+                                         int height, int width) {
+  if (out_channels != 256 || batch_size <= 0 || in_channels <= 0 || in_channels % 8 != 0 ||
+      height <= 0 || width <= 0) {
+    g_last_error = "fpn_auto_tune_lateral_conv: need out_channels = 256, Cin % 8 == 0";
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lk(g_tune_mu);
+  auto key = std::make_tuple(batch_size, in_channels, out_channels, height, width);
+  auto it = g_tune_results.find(key);
+  if (it != g_tune_results.end()) return &it->second;
+  const size_t px = static_cast<size_t>(batch_size) * height * width;
+  void *x = nullptr, *w = nullptr, *o = nullptr;
+  float* b = nullptr;
+  TuningResult res{};
+  bool ok = cudaMalloc(&x, px * in_channels * 2) == cudaSuccess &&
+            cudaMalloc(&w, static_cast<size_t>(256) * in_channels * 2) == cudaSuccess &&
+            cudaMalloc(&o, px * 256 * 2) == cudaSuccess &&
+            cudaMalloc(&b, 256 * sizeof(float)) == cudaSuccess;
+  if (ok) {
+    cudaMemset(x, 0, px * in_channels * 2);
+    cudaMemset(w, 0, static_cast<size_t>(256) * in_channels * 2);
+    cudaMemset(b, 0, 256 * sizeof(float));
+    const int sms = ufpn::sm_count();
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    float best = -1.f;
+    for (int ctas : {sms, sms / 2, 2 * sms / 3}) {
+      ufpn::TcPlan plan;
+      if (ufpn::plan_tc_lateral(plan, DType::BF16, x, w, b, nullptr, o, batch_size, in_channels,
+                                height, width, 0, 0, device_status_word(), ctas) != cudaSuccess)
+        continue;
+      ufpn::launch_tc(plan, 0);
+      cudaEventRecord(e0, 0);
+      for (int i = 0; i < 10; ++i) ufpn::launch_tc(plan, 0);
+      cudaEventRecord(e1, 0);
+      if (cudaEventSynchronize(e1) != cudaSuccess) break;
+      float ms = 0.f;
+      cudaEventElapsedTime(&ms, e0, e1);
+      ms /= 10.f;
+      if (best < 0 || ms < best) {
+        best = ms;
+        res.num_ctas = plan.grid;
+      }
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    res.time_ms = best;
+    const double flops = 2.0 * px * 256 * in_channels;
+    const double bytes = (px * (in_channels + 256) + 256.0 * in_channels) * 2;
+    res.performance_gflops = best > 0 ? static_cast<float>(flops / (best * 1e-3) / 1e9) : 0.f;
+    res.memory_bandwidth_gb_s = best > 0 ? static_cast<float>(bytes / (best * 1e-3) / 1e9) : 0.f;
+    std::snprintf(res.architecture_name, sizeof(res.architecture_name), "sm_100a");
+    ok = best > 0;
+  }
+  cudaFree(x);
+  cudaFree(w);
+  cudaFree(o);
+  cudaFree(b);
+  if (!ok) {
+    g_last_error = "fpn_auto_tune_lateral_conv: allocation or launch failed";
+    return nullptr;
+  }
+  auto ins = g_tune_results.emplace(key, res);
+  return &ins.first->second;
+}
+
+void fpn_auto_tune_save_results(const char* filename) {
+  if (!filename) return;
+  std::lock_guard<std::mutex> lk(g_tune_mu);
+  std::ofstream f(filename);
+  f << "batch,in_channels,out_channels,height,width,num_ctas,time_ms,gflops,gb_s,arch\n";
+  for (auto& kv : g_tune_results) {
+    const auto& k = kv.first;
+    const auto& r = kv.second;
+    f << std::get<0>(k) << "," << std::get<1>(k) << "," << std::get<2>(k) << ","
+      << std::get<3>(k) << "," << std::get<4>(k) << "," << r.num_ctas << "," << r.time_ms << ","
+      << r.performance_gflops << "," << r.memory_bandwidth_gb_s << "," << r.architecture_name
+      << "\n";
+  }
+}
+
+}  // extern "C"

@@ -1,0 +1,703 @@
+// UnifiedFPNCore: the FPN neck engine.
+//
+// Reference: lib/core/fpn_engine.cu:10-416 (class UnifiedFPNCore).  The
+// reference ran a 4-level lateral loop then a top-down loop on four private
+// streams with no ordering between level l+1's output and level l's upsample
+// (fpn_engine.cu:223-235) and a blocking host sync every call (:239-241).
+// This engine instead enqueues, on the caller's stream:
+//
+//   main stream:  lat5 -> lat4 -> lat3 -> lat2          (each lateral epilogue
+//                  |       |       |       |             reads M_{l+1} written
+//   side stream:  3x3_5   3x3_4   3x3_3   3x3_2 (+P6)   by the previous one)
+//
+// i.e. the top-down chain stays on one stream (true data dependence) while each
+// level's 3x3 output conv runs on a side stream as soon as its merged map M_l
+// exists, overlapping the next lateral.  The whole schedule is captured once
+// per (pointer set) into a CUDA graph on a private stream and replayed with a
+// single cudaGraphLaunch on the caller's stream.
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <map>
+#include <sstream>
+#include <string>
+#include <vector>
+
+#include "kernels.h"
+#include "unified_fpn/core/engine.h"
+
+using ufpn::Conv3x3Tiling;
+using ufpn::DType;
+using ufpn::Layout;
+using ufpn::TcPlan;
+
+namespace {
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+DType to_dtype(FPNDataType t) {
+  switch (t) {
+    case FPNDataType::FLOAT32:
+      return DType::F32;
+    case FPNDataType::FLOAT16:
+      return DType::F16;
+    case FPNDataType::BFLOAT16:
+      return DType::BF16;
+    default:
+      FPN_THROW("unsupported dtype: the neck runs in FLOAT32, FLOAT16 or BFLOAT16");
+  }
+}
+
+// Heuristic 3x3 tiling: the tile_w in {8..128} that wastes the fewest padded
+// pixels (ties go to 16, then to the wider tile).
+Conv3x3Tiling heuristic_tiling(int H, int W) {
+  Conv3x3Tiling best;
+  long long best_area = -1;
+  for (int tw : {16, 8, 32, 64, 128}) {
+    const int th = 128 / tw;
+    const long long area = static_cast<long long>((W + tw - 1) / tw) * tw *
+                           static_cast<long long>((H + th - 1) / th) * th;
+    if (best_area < 0 || area < best_area) {
+      best_area = area;
+      best.tile_w = tw;
+      best.tile_h = th;
+    }
+  }
+  return best;
+}
+
+}  // namespace
+
+struct UnifiedFPNCore::Impl {
+  int device = 0;
+  size_t workspace_cap = 0;
+  int cout = 256;
+  DType dtype = DType::F32;
+  Layout layout = Layout::NCHW;
+  int batch = 0;
+  int cin[4] = {};
+  int H[4] = {};
+  int W[4] = {};
+  bool configured = false;
+  int w_cin[4] = {};  // Cin the weight buffers were allocated for
+  bool weights_allocated = false;
+  bool weights_set[4] = {};
+  float* lat_w32[4] = {};
+  float* lat_b[4] = {};
+  float* out_w32[4] = {};
+  float* out_b[4] = {};
+  void* lat_wp[4] = {};
+  void* out_wp[4] = {};
+  DType packed_dtype = DType::F32;
+  void* merged[4] = {};
+  void* nhwc_in[4] = {};
+  void* nhwc_out[5] = {};
+  size_t workspace_bytes = 0;
+  size_t weight_bytes = 0;
+  int* d_status = nullptr;
+  cudaStream_t side = nullptr;
+  cudaStream_t capture = nullptr;
+  cudaStream_t setup = nullptr;
+  cudaEvent_t ev_fork = nullptr;
+  cudaEvent_t ev_lat[4] = {};
+  cudaEvent_t ev_join = nullptr;
+  cudaEvent_t prof[10] = {};
+  FPNKernelConfig cfg;
+  Conv3x3Tiling tiling[4];
+  bool tiling_tuned[4] = {};
+  bool profiling = false;
+  FPNPerformanceMetrics metrics{};
+  struct GraphEntry {
+    const void* in[4];
+    void* out[4];
+    void* p6;
+    cudaGraphExec_t exec;
+    int launches;
+  };
+  std::vector<GraphEntry> graphs;
+  std::map<std::string, std::pair<int, float>> tuning_db;  // key -> (tile_w, ms)
+
+  ~Impl() { release_all(); }
+
+  void release_graphs() {
+    for (auto& g : graphs) cudaGraphExecDestroy(g.exec);
+    graphs.clear();
+  }
+  void free_workspace() {
+    for (int l = 0; l < 4; ++l) {
+      cudaFree(merged[l]);
+      cudaFree(nhwc_in[l]);
+      merged[l] = nhwc_in[l] = nullptr;
+    }
+    for (int l = 0; l < 5; ++l) {
+      cudaFree(nhwc_out[l]);
+      nhwc_out[l] = nullptr;
+    }
+    workspace_bytes = 0;
+  }
+  void free_weights() {
+    for (int l = 0; l < 4; ++l) {
+      cudaFree(lat_w32[l]);
+      cudaFree(lat_b[l]);
+      cudaFree(out_w32[l]);
+      cudaFree(out_b[l]);
+      cudaFree(lat_wp[l]);
+      cudaFree(out_wp[l]);
+      lat_w32[l] = lat_b[l] = out_w32[l] = out_b[l] = nullptr;
+      lat_wp[l] = out_wp[l] = nullptr;
+      weights_set[l] = false;
+    }
+    weights_allocated = false;
+    weight_bytes = 0;
+  }
+  void release_all() {
+    DeviceGuard g(device);
+    release_graphs();
+    free_workspace();
+    free_weights();
+    cudaFree(d_status);
+    d_status = nullptr;
+    if (side) cudaStreamDestroy(side);
+    if (capture) cudaStreamDestroy(capture);
+    if (setup) cudaStreamDestroy(setup);
+    side = capture = setup = nullptr;
+    if (ev_fork) cudaEventDestroy(ev_fork);
+    if (ev_join) cudaEventDestroy(ev_join);
+    for (auto& e : ev_lat)
+      if (e) cudaEventDestroy(e);
+    for (auto& e : prof)
+      if (e) cudaEventDestroy(e);
+  }
+
+  bool tensor_core_path() const { return dtype != DType::F32 && cfg.use_tensor_cores; }
+
+  std::string tuning_key(int l) const {
+    std::ostringstream k;
+    k << "conv3x3/" << static_cast<int>(dtype) << "/" << batch << "x" << H[l] << "x" << W[l]
+      << "/sm" << ufpn::sm_count();
+    return k.str();
+  }
+
+  Conv3x3Tiling tiling_for(int l) const {
+    if (cfg.tile_size > 0 && 128 % cfg.tile_size == 0 && cfg.tile_size <= 128) {
+      Conv3x3Tiling t;
+      t.tile_w = cfg.tile_size;
+      t.tile_h = 128 / cfg.tile_size;
+      return t;
+    }
+    return tiling[l];
+  }
+
+  void check(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) FPN_THROW(std::string(what) + ": " + cudaGetErrorString(e));
+  }
+
+  void ensure_weight_packing() {
+    if (!tensor_core_path() || packed_dtype == dtype) return;
+    for (int l = 0; l < 4; ++l) {
+      cudaFree(lat_wp[l]);
+      cudaFree(out_wp[l]);
+      lat_wp[l] = out_wp[l] = nullptr;
+      const size_t esz = ufpn::dtype_size(dtype);
+      check(cudaMalloc(&lat_wp[l], static_cast<size_t>(cout) * w_cin[l] * esz), "cudaMalloc");
+      check(cudaMalloc(&out_wp[l], static_cast<size_t>(cout) * cout * 9 * esz), "cudaMalloc");
+      if (weights_set[l]) pack_level(l);
+    }
+    packed_dtype = dtype;
+  }
+
+  void pack_level(int l) {
+    if (!tensor_core_path()) return;
+    check(ufpn::launch_convert_weights(dtype, lat_w32[l], lat_wp[l],
+                                       static_cast<long long>(cout) * w_cin[l], setup),
+          "pack lateral weights");
+    check(ufpn::launch_pack_conv3x3(dtype, out_w32[l], out_wp[l], cout, cout, setup),
+          "pack 3x3 weights");
+    check(cudaStreamSynchronize(setup), "weight packing");
+  }
+
+  // ------------------------------------------------------------ the schedule
+  // Enqueues the whole neck on `main`; returns the number of kernels launched.
+  int enqueue(const void* const* in, void* const* out, void* p6, cudaStream_t main,
+              bool prof_events) {
+    int launches = 0;
+    auto ok = [&](cudaError_t e, const char* what) {
+      check(e, what);
+      ++launches;
+    };
+    if (!tensor_core_path()) {
+      // fp32 CUDA-core path, NCHW, all on one stream.
+      if (prof_events) cudaEventRecord(prof[0], main);
+      for (int l = 3; l >= 0; --l) {
+        const float* coarse = l < 3 ? static_cast<const float*>(merged[l + 1]) : nullptr;
+        ok(ufpn::launch_fp32_lateral(static_cast<const float*>(in[l]), lat_w32[l], lat_b[l],
+                                     coarse, static_cast<float*>(merged[l]), batch, cin[l], cout,
+                                     H[l], W[l], l < 3 ? H[l + 1] : 1, l < 3 ? W[l + 1] : 1, main),
+           "fp32 lateral");
+        if (prof_events) cudaEventRecord(prof[1 + 2 * (3 - l)], main);
+        ok(ufpn::launch_fp32_conv3x3(static_cast<const float*>(merged[l]), out_w32[l], out_b[l],
+                                     static_cast<float*>(out[l]), batch, cout, cout, H[l], W[l],
+                                     main),
+           "fp32 conv3x3");
+        if (l == 3 && p6)
+          ok(ufpn::launch_p6(DType::F32, out[3], p6, batch, cout, H[3], W[3], Layout::NCHW, main),
+             "p6");
+        if (prof_events) cudaEventRecord(prof[2 + 2 * (3 - l)], main);
+      }
+      return launches;
+    }
+
+    const bool nchw = layout == Layout::NCHW;
+    const void* x[4];
+    void* o[4];
+    void* o6 = p6 ? (nchw ? nhwc_out[4] : p6) : nullptr;
+    for (int l = 0; l < 4; ++l) {
+      o[l] = nchw ? nhwc_out[l] : out[l];
+      x[l] = in[l];
+    }
+    if (prof_events) cudaEventRecord(prof[0], main);
+    if (nchw) {
+      for (int l = 3; l >= 0; --l) {
+        ok(ufpn::launch_transpose(dtype, in[l], nhwc_in[l], batch, cin[l], H[l] * W[l], true,
+                                  main),
+           "NCHW->NHWC");
+        x[l] = nhwc_in[l];
+      }
+    }
+    cudaStream_t conv_stream = prof_events ? main : side;
+    if (!prof_events) {
+      check(cudaEventRecord(ev_fork, main), "event");
+      check(cudaStreamWaitEvent(side, ev_fork, 0), "event");
+    }
+    for (int l = 3; l >= 0; --l) {
+      TcPlan lat;
+      check(ufpn::plan_tc_lateral(lat, dtype, x[l], lat_wp[l], lat_b[l],
+                                  l < 3 ? merged[l + 1] : nullptr, merged[l], batch, cin[l], H[l],
+                                  W[l], l < 3 ? H[l + 1] : 0, l < 3 ? W[l + 1] : 0, d_status, 0),
+            "plan lateral");
+      ok(ufpn::launch_tc(lat, main), "lateral launch");
+      if (prof_events) cudaEventRecord(prof[1 + 2 * (3 - l)], main);
+      if (!prof_events) {
+        check(cudaEventRecord(ev_lat[l], main), "event");
+        check(cudaStreamWaitEvent(side, ev_lat[l], 0), "event");
+      }
+      TcPlan conv;
+      check(ufpn::plan_tc_conv3x3(conv, dtype, merged[l], out_wp[l], out_b[l], o[l],
+                                  l == 3 ? o6 : nullptr, batch, H[l], W[l], tiling_for(l),
+                                  d_status, 0),
+            "plan conv3x3");
+      ok(ufpn::launch_tc(conv, conv_stream), "conv3x3 launch");
+      if (prof_events) cudaEventRecord(prof[2 + 2 * (3 - l)], main);
+    }
+    if (nchw) {
+      for (int l = 0; l < 4; ++l)
+        ok(ufpn::launch_transpose(dtype, o[l], out[l], batch, cout, H[l] * W[l], false,
+                                  conv_stream),
+           "NHWC->NCHW");
+      if (p6)
+        ok(ufpn::launch_transpose(dtype, o6, p6, batch, cout,
+                                  ((H[3] - 1) / 2 + 1) * ((W[3] - 1) / 2 + 1), false, conv_stream),
+           "NHWC->NCHW");
+    }
+    if (!prof_events) {
+      check(cudaEventRecord(ev_join, side), "event");
+      check(cudaStreamWaitEvent(main, ev_join, 0), "event");
+    }
+    return launches;
+  }
+
+  double flops() const {
+    double f = 0;
+    for (int l = 0; l < 4; ++l) {
+      const double px = static_cast<double>(batch) * H[l] * W[l];
+      f += 2.0 * px * cout * cin[l] + 2.0 * px * cout * cout * 9;
+    }
+    return f;
+  }
+  double compulsory_bytes() const {
+    const double esz = ufpn::dtype_size(dtype);
+    double b = 0;
+    for (int l = 0; l < 4; ++l) {
+      const double px = static_cast<double>(batch) * H[l] * W[l];
+      b += px * cin[l] * esz + px * cout * esz;              // read C_l, write P_l
+      b += (static_cast<double>(cout) * cin[l] + 9.0 * cout * cout) * esz;  // weights
+    }
+    return b;
+  }
+};
+
+UnifiedFPNCore::UnifiedFPNCore(size_t workspace_size, int device) : impl_(new Impl) {
+  if (device < 0) CUDA_CHECK(cudaGetDevice(&device));
+  impl_->device = device;
+  impl_->workspace_cap = workspace_size;
+  DeviceGuard g(device);
+  CUDA_CHECK(cudaStreamCreateWithFlags(&impl_->side, cudaStreamNonBlocking));
+  CUDA_CHECK(cudaStreamCreateWithFlags(&impl_->capture, cudaStreamNonBlocking));
+  CUDA_CHECK(cudaStreamCreateWithFlags(&impl_->setup, cudaStreamNonBlocking));
+  CUDA_CHECK(cudaEventCreateWithFlags(&impl_->ev_fork, cudaEventDisableTiming));
+  CUDA_CHECK(cudaEventCreateWithFlags(&impl_->ev_join, cudaEventDisableTiming));
+  for (auto& e : impl_->ev_lat) CUDA_CHECK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  for (auto& e : impl_->prof) CUDA_CHECK(cudaEventCreate(&e));
+  CUDA_CHECK(cudaMalloc(&impl_->d_status, 256));
+  CUDA_CHECK(cudaMemset(impl_->d_status, 0, 256));
+}
+
+UnifiedFPNCore::~UnifiedFPNCore() = default;
+
+void UnifiedFPNCore::configure_levels(const std::vector<FPNDimensions>& dims, int output_channels,
+                                      FPNDataType dtype, FPNLayout layout) {
+  Impl& m = *impl_;
+  if (dims.size() != 4 && dims.size() != 5)
+    FPN_THROW("configure_levels expects the dimensions of C2..C5 (or C2..C6)");
+  if (output_channels != 256)
+    FPN_THROW("only output_channels = 256 is supported (the tensor-core tile is 256 wide)");
+  const DType dt = to_dtype(dtype);
+  const Layout lay = layout == FPNLayout::NHWC ? Layout::NHWC : Layout::NCHW;
+  if (dt == DType::F32 && lay != Layout::NCHW)
+    FPN_THROW("the fp32 path takes NCHW (contiguous) tensors");
+  const int N = dims[0].batch_size;
+  for (int l = 0; l < 4; ++l) {
+    if (dims[l].batch_size != N) FPN_THROW("all levels must share the batch size");
+    if (dims[l].channels <= 0 || dims[l].height <= 0 || dims[l].width <= 0)
+      FPN_THROW("level dimensions must be positive");
+    if (dt != DType::F32 && dims[l].channels % 8 != 0)
+      FPN_THROW("16-bit inputs need Cin % 8 == 0 (16-byte TMA row stride)");
+    if (l < 3 && (dims[l + 1].height > dims[l].height || dims[l + 1].width > dims[l].width))
+      FPN_THROW("levels must be ordered fine (C2) to coarse (C5)");
+  }
+  DeviceGuard g(m.device);
+  bool same = m.configured && m.batch == N && m.dtype == dt && m.layout == lay;
+  for (int l = 0; l < 4 && same; ++l)
+    same = m.cin[l] == dims[l].channels && m.H[l] == dims[l].height && m.W[l] == dims[l].width;
+  if (same) return;
+  m.release_graphs();
+  m.free_workspace();
+  m.batch = N;
+  m.dtype = dt;
+  m.layout = lay;
+  m.cout = output_channels;
+  for (int l = 0; l < 4; ++l) {
+    m.cin[l] = dims[l].channels;
+    m.H[l] = dims[l].height;
+    m.W[l] = dims[l].width;
+    m.tiling[l] = heuristic_tiling(m.H[l], m.W[l]);
+    m.tiling_tuned[l] = false;
+    auto it = m.tuning_db.find(m.tuning_key(l));
+    if (it != m.tuning_db.end()) {
+      m.tiling[l].tile_w = it->second.first;
+      m.tiling[l].tile_h = 128 / it->second.first;
+      m.tiling_tuned[l] = true;
+    }
+  }
+  const size_t esz = ufpn::dtype_size(dt);
+  size_t total = 0;
+  for (int l = 0; l < 4; ++l) {
+    const size_t px = static_cast<size_t>(N) * m.H[l] * m.W[l];
+    m.check(cudaMalloc(&m.merged[l], px * m.cout * esz), "workspace");
+    total += px * m.cout * esz;
+    if (m.tensor_core_path() && lay == Layout::NCHW) {
+      m.check(cudaMalloc(&m.nhwc_in[l], px * m.cin[l] * esz), "workspace");
+      m.check(cudaMalloc(&m.nhwc_out[l], px * m.cout * esz), "workspace");
+      total += px * (m.cin[l] + m.cout) * esz;
+    }
+  }
+  if (m.tensor_core_path() && lay == Layout::NCHW) {
+    const size_t px6 = static_cast<size_t>(N) * ((m.H[3] - 1) / 2 + 1) * ((m.W[3] - 1) / 2 + 1);
+    m.check(cudaMalloc(&m.nhwc_out[4], px6 * m.cout * esz), "workspace");
+    total += px6 * m.cout * esz;
+  }
+  m.workspace_bytes = total;
+  m.configured = true;
+  if (m.weights_allocated) {
+    m.packed_dtype = DType::F32;  // force repack in the new dtype
+    m.ensure_weight_packing();
+  }
+}
+
+void UnifiedFPNCore::allocate_weights(const std::vector<int>& channels, int output_channels) {
+  Impl& m = *impl_;
+  if (output_channels != 256) FPN_THROW("only output_channels = 256 is supported");
+  std::vector<int> c = channels;
+  if (c.size() == 5) c.erase(c.begin());  // reference form {C1 (unused), C2..C5}
+  if (c.size() != 4) FPN_THROW("allocate_weights expects the channels of C2..C5");
+  DeviceGuard g(m.device);
+  m.release_graphs();
+  m.free_weights();
+  m.cout = output_channels;
+  size_t bytes = 0;
+  for (int l = 0; l < 4; ++l) {
+    if (c[l] <= 0) FPN_THROW("channel counts must be positive");
+    m.w_cin[l] = c[l];
+    const size_t lw = static_cast<size_t>(m.cout) * c[l];
+    const size_t ow = static_cast<size_t>(m.cout) * m.cout * 9;
+    m.check(cudaMalloc(&m.lat_w32[l], lw * 4), "weights");
+    m.check(cudaMalloc(&m.lat_b[l], m.cout * 4), "weights");
+    m.check(cudaMalloc(&m.out_w32[l], ow * 4), "weights");
+    m.check(cudaMalloc(&m.out_b[l], m.cout * 4), "weights");
+    bytes += (lw + ow + 2 * m.cout) * 4;
+    if (m.configured && m.tensor_core_path()) bytes += (lw + ow) * ufpn::dtype_size(m.dtype);
+  }
+  m.weight_bytes = bytes;
+  m.weights_allocated = true;
+  m.packed_dtype = DType::F32;
+  m.ensure_weight_packing();
+}
+
+void UnifiedFPNCore::set_weights(int level, const float* lw, const float* lb, const float* ow,
+                                 const float* ob) {
+  Impl& m = *impl_;
+  if (!m.weights_allocated || level < 0 || level >= 4)
+    FPN_THROW("Invalid level or weights not allocated");
+  if (!lw || !lb || !ow || !ob) FPN_THROW("null weight pointer");
+  DeviceGuard g(m.device);
+  const size_t lwn = static_cast<size_t>(m.cout) * m.w_cin[level];
+  const size_t own = static_cast<size_t>(m.cout) * m.cout * 9;
+  m.check(cudaMemcpyAsync(m.lat_w32[level], lw, lwn * 4, cudaMemcpyDefault, m.setup), "copy");
+  m.check(cudaMemcpyAsync(m.lat_b[level], lb, m.cout * 4, cudaMemcpyDefault, m.setup), "copy");
+  m.check(cudaMemcpyAsync(m.out_w32[level], ow, own * 4, cudaMemcpyDefault, m.setup), "copy");
+  m.check(cudaMemcpyAsync(m.out_b[level], ob, m.cout * 4, cudaMemcpyDefault, m.setup), "copy");
+  m.check(cudaStreamSynchronize(m.setup), "copy");
+  m.weights_set[level] = true;
+  m.release_graphs();
+  if (m.configured && m.tensor_core_path()) {
+    m.ensure_weight_packing();
+    m.pack_level(level);
+  }
+}
+
+void UnifiedFPNCore::forward_raw(const void* const* in, void* const* out, void* p6,
+                                 cudaStream_t stream) {
+  Impl& m = *impl_;
+  if (!m.configured) FPN_THROW("configure_levels() has not been called");
+  for (int l = 0; l < 4; ++l) {
+    if (!m.weights_set[l]) FPN_THROW("Weights not initialized");
+    if (m.w_cin[l] != m.cin[l]) FPN_THROW("weights were allocated for different channel counts");
+    if (!in[l] || !out[l]) FPN_THROW("null input/output pointer");
+  }
+  DeviceGuard g(m.device);
+  m.ensure_weight_packing();
+  if (m.profiling) {
+    const int n = m.enqueue(in, out, p6, stream, true);
+    m.check(cudaEventRecord(m.prof[9], stream), "event");
+    m.check(cudaEventSynchronize(m.prof[9]), "event");
+    float total = 0.f;
+    for (int k = 0; k < 8; ++k) {
+      float t = 0.f;
+      cudaEventElapsedTime(&t, m.prof[k], m.prof[k + 1]);
+      m.metrics.kernel_times_ms[k] = t;
+    }
+    cudaEventElapsedTime(&total, m.prof[0], m.prof[9]);
+    m.metrics.forward_time_ms = total;
+    m.metrics.memory_bandwidth_gb_s =
+        total > 0 ? static_cast<float>(m.compulsory_bytes() / (total * 1e-3) / 1e9) : 0.f;
+    const double peak = m.tensor_core_path() ? 2.25e15 : 8.0e13;  // nominal dense peaks
+    m.metrics.compute_utilization =
+        total > 0 ? static_cast<float>(m.flops() / (total * 1e-3) / peak) : 0.f;
+    m.metrics.num_kernel_launches = n;
+    m.metrics.peak_memory_usage_bytes = m.workspace_bytes + m.weight_bytes;
+    m.profiling = false;
+    return;
+  }
+  if (m.cfg.enable_graph_capture) {
+    for (auto& e : m.graphs) {
+      if (e.p6 != p6) continue;
+      bool hit = true;
+      for (int l = 0; l < 4 && hit; ++l) hit = e.in[l] == in[l] && e.out[l] == out[l];
+      if (hit) {
+        m.check(cudaGraphLaunch(e.exec, stream), "cudaGraphLaunch");
+        m.metrics.num_kernel_launches = e.launches;
+        return;
+      }
+    }
+    // Capture on the private stream (capturing the legacy default stream is not
+    // allowed), ordered after the caller's prior work by the graph launch itself.
+    cudaGraph_t graph = nullptr;
+    m.check(cudaStreamBeginCapture(m.capture, cudaStreamCaptureModeThreadLocal), "capture");
+    int n = 0;
+    try {
+      n = m.enqueue(in, out, p6, m.capture, false);
+    } catch (...) {
+      cudaStreamEndCapture(m.capture, &graph);
+      if (graph) cudaGraphDestroy(graph);
+      throw;
+    }
+    m.check(cudaStreamEndCapture(m.capture, &graph), "capture");
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    m.check(ie, "cudaGraphInstantiate");
+    if (m.graphs.size() >= 8) {
+      cudaGraphExecDestroy(m.graphs.front().exec);
+      m.graphs.erase(m.graphs.begin());
+    }
+    Impl::GraphEntry e;
+    for (int l = 0; l < 4; ++l) {
+      e.in[l] = in[l];
+      e.out[l] = out[l];
+    }
+    e.p6 = p6;
+    e.exec = exec;
+    e.launches = n;
+    m.graphs.push_back(e);
+    m.check(cudaGraphLaunch(exec, stream), "cudaGraphLaunch");
+    m.metrics.num_kernel_launches = n;
+    return;
+  }
+  m.metrics.num_kernel_launches = m.enqueue(in, out, p6, stream, false);
+}
+
+template <typename T>
+void UnifiedFPNCore::forward(const std::vector<FPNTensor<T>>& features,
+                             std::vector<FPNTensor<T>>& outputs, cudaStream_t stream) {
+  if (features.size() != 4 && features.size() != 5)
+    FPN_THROW("forward expects C2..C5 (or C2..C6) feature tensors");
+  if (outputs.size() != 4 && outputs.size() != 5)
+    FPN_THROW("forward expects P2..P5 (or P2..P6) output tensors");
+  const void* in[4];
+  void* out[4];
+  for (int l = 0; l < 4; ++l) {
+    in[l] = features[l].data;
+    out[l] = outputs[l].data;
+  }
+  forward_raw(in, out, outputs.size() == 5 ? outputs[4].data : nullptr, stream);
+}
+
+template void UnifiedFPNCore::forward<float>(const std::vector<FPNTensor<float>>&,
+                                             std::vector<FPNTensor<float>>&, cudaStream_t);
+template void UnifiedFPNCore::forward<void>(const std::vector<FPNTensor<void>>&,
+                                            std::vector<FPNTensor<void>>&, cudaStream_t);
+
+const FPNPerformanceMetrics& UnifiedFPNCore::get_performance_metrics() const {
+  return impl_->metrics;
+}
+
+void UnifiedFPNCore::set_kernel_config(const FPNKernelConfig& config) {
+  if (config.activation != FPNActivation::NONE)
+    FPN_THROW("the standard FPN neck has no activation; only FPNActivation::NONE is supported");
+  if (config.tile_size != 0 &&
+      (config.tile_size < 1 || config.tile_size > 128 || 128 % config.tile_size != 0))
+    FPN_THROW("tile_size must divide 128 (8, 16, 32, 64, 128) or be 0 for automatic");
+  impl_->release_graphs();
+  impl_->cfg = config;
+}
+
+size_t UnifiedFPNCore::get_memory_usage() const {
+  return impl_->workspace_bytes + impl_->weight_bytes;
+}
+
+void UnifiedFPNCore::set_profiling(bool enable) { impl_->profiling = enable; }
+
+int UnifiedFPNCore::device_status(bool reset) {
+  DeviceGuard g(impl_->device);
+  int v = 0;
+  CUDA_CHECK(cudaDeviceSynchronize());
+  CUDA_CHECK(cudaMemcpy(&v, impl_->d_status, sizeof(int), cudaMemcpyDeviceToHost));
+  if (reset) CUDA_CHECK(cudaMemset(impl_->d_status, 0, sizeof(int)));
+  return v;
+}
+
+std::string UnifiedFPNCore::autotune(const void* const* in, void* const* out, void* p6,
+                                     cudaStream_t stream, int iterations) {
+  Impl& m = *impl_;
+  if (!m.configured) FPN_THROW("configure_levels() has not been called");
+  std::ostringstream rep;
+  if (!m.tensor_core_path()) {
+    rep << "fp32 path: nothing to tune\n";
+    return rep.str();
+  }
+  DeviceGuard g(m.device);
+  // One plain forward so the merged maps hold real data.
+  const bool saved_graph = m.cfg.enable_graph_capture;
+  m.cfg.enable_graph_capture = false;
+  forward_raw(in, out, p6, stream);
+  m.cfg.enable_graph_capture = saved_graph;
+  CUDA_CHECK(cudaStreamSynchronize(stream));
+  if (iterations < 1) iterations = 1;
+  for (int l = 3; l >= 0; --l) {
+    float best_ms = -1.f;
+    int best_tw = m.tiling[l].tile_w;
+    for (int tw : {8, 16, 32, 64, 128}) {
+      if (tw > 2 * m.W[l] && tw != 8) continue;  // wider than the image: pure padding
+      Conv3x3Tiling t;
+      t.tile_w = tw;
+      t.tile_h = 128 / tw;
+      TcPlan conv;
+      const bool nchw = m.layout == Layout::NCHW;
+      void* o = nchw ? m.nhwc_out[l] : out[l];
+      if (ufpn::plan_tc_conv3x3(conv, m.dtype, m.merged[l], m.out_wp[l], m.out_b[l], o, nullptr,
+                                m.batch, m.H[l], m.W[l], t, m.d_status, 0) != cudaSuccess)
+        continue;
+      CUDA_CHECK(ufpn::launch_tc(conv, stream));  // warm-up
+      CUDA_CHECK(cudaEventRecord(m.prof[0], stream));
+      for (int i = 0; i < iterations; ++i) CUDA_CHECK(ufpn::launch_tc(conv, stream));
+      CUDA_CHECK(cudaEventRecord(m.prof[1], stream));
+      CUDA_CHECK(cudaEventSynchronize(m.prof[1]));
+      float ms = 0.f;
+      cudaEventElapsedTime(&ms, m.prof[0], m.prof[1]);
+      ms /= iterations;
+      rep << "P" << (l + 2) << " 3x3 " << m.batch << "x" << m.H[l] << "x" << m.W[l] << " tile "
+          << tw << "x" << 128 / tw << ": " << ms * 1e3 << " us\n";
+      if (best_ms < 0 || ms < best_ms) {
+        best_ms = ms;
+        best_tw = tw;
+      }
+    }
+    m.tiling[l].tile_w = best_tw;
+    m.tiling[l].tile_h = 128 / best_tw;
+    m.tiling_tuned[l] = true;
+    m.tuning_db[m.tuning_key(l)] = {best_tw, best_ms};
+    rep << "P" << (l + 2) << " -> tile " << best_tw << "x" << 128 / best_tw << "\n";
+  }
+  m.release_graphs();
+  if (device_status(true) != 0) FPN_THROW("device pipeline timeout during autotuning");
+  return rep.str();
+}
+
+bool UnifiedFPNCore::save_tuning(const std::string& path) const {
+  std::ofstream f(path);
+  if (!f) return false;
+  f << "ufpn-tuning 1\n";
+  for (auto& kv : impl_->tuning_db)
+    f << kv.first << " " << kv.second.first << " " << kv.second.second << "\n";
+  return static_cast<bool>(f);
+}
+
+bool UnifiedFPNCore::load_tuning(const std::string& path) {
+  std::ifstream f(path);
+  if (!f) return false;
+  std::string magic;
+  int ver = 0;
+  f >> magic >> ver;
+  if (magic != "ufpn-tuning" || ver != 1) return false;
+  std::string key;
+  int tw;
+  float ms;
+  while (f >> key >> tw >> ms) {
+    if (tw > 0 && tw <= 128 && 128 % tw == 0) impl_->tuning_db[key] = {tw, ms};
+  }
+  Impl& m = *impl_;
+  if (m.configured) {
+    for (int l = 0; l < 4; ++l) {
+      auto it = m.tuning_db.find(m.tuning_key(l));
+      if (it != m.tuning_db.end()) {
+        m.tiling[l].tile_w = it->second.first;
+        m.tiling[l].tile_h = 128 / it->second.first;
+        m.tiling_tuned[l] = true;
+      }
+    }
+    m.release_graphs();
+  }
+  return true;
+}

@@ -1,0 +1,521 @@
+// Bandwidth-bound FPN kernels (upsample-add, P6, layout conversion, weight
+// packing) and the fp32 CUDA-core path (1x1 lateral + fused upsample-add, 3x3).
+//
+// Bilinear semantics follow the reference's host implementation
+// benchmarks/upsample_benchmark.cu:24-108 and its device helper
+// lib/kernels/compute/fpn_compute_kernels.cu:21-59: half-pixel source
+// coordinate (o + 0.5) * in/out - 0.5 (or o * (in-1)/(out-1) with
+// align_corners), clamped to [0, in-1], y1 = min(y0+1, in-1), weights
+// (1-wy)(1-wx), (1-wy)wx, wy(1-wx), wy*wx.
+#include "kernels.h"
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+namespace ufpn {
+
+namespace {
+
+template <typename T>
+__device__ __forceinline__ float to_f(T v);
+template <>
+__device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
+template <>
+__device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+template <typename T>
+__device__ __forceinline__ T from_f(float v);
+template <>
+__device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+struct BilinearTap {
+  int y0, y1, x0, x1;
+  float w00, w01, w10, w11;
+};
+
+__device__ __forceinline__ float src_coord(int o, int in, int out, float scale, int align_corners) {
+  float s;
+  if (align_corners) {
+    s = out > 1 ? static_cast<float>(o) * scale : 0.f;
+  } else {
+    s = (static_cast<float>(o) + 0.5f) * scale - 0.5f;
+  }
+  return fminf(fmaxf(s, 0.f), static_cast<float>(in - 1));
+}
+
+__device__ __forceinline__ BilinearTap make_tap(int y, int x, int Hc, int Wc, int H, int W,
+                                                float sy_scale, float sx_scale, int ac) {
+  const float sy = src_coord(y, Hc, H, sy_scale, ac);
+  const float sx = src_coord(x, Wc, W, sx_scale, ac);
+  BilinearTap t;
+  t.y0 = static_cast<int>(sy);
+  t.x0 = static_cast<int>(sx);
+  t.y1 = min(t.y0 + 1, Hc - 1);
+  t.x1 = min(t.x0 + 1, Wc - 1);
+  const float wy = sy - static_cast<float>(t.y0);
+  const float wx = sx - static_cast<float>(t.x0);
+  t.w00 = (1.f - wy) * (1.f - wx);
+  t.w01 = (1.f - wy) * wx;
+  t.w10 = wy * (1.f - wx);
+  t.w11 = wy * wx;
+  return t;
+}
+
+// Vector of 16 bytes viewed as elements of T.
+template <typename T>
+struct Vec16 {
+  static constexpr int kN = 16 / sizeof(T);
+  union {
+    uint4 u;
+    T e[kN];
+  };
+};
+
+// ---------------------------------------------------------------- NHWC upsample-add
+// out[n,y,x,c] = lat[n,y,x,c] (or 0) + bilinear(coarse)[n,y,x,c].  One thread per
+// 16-byte channel vector; consecutive threads walk channels of one pixel, so every
+// load and store of a warp is a contiguous, fully coalesced 512-byte segment.
+template <typename T, bool kVec>
+__global__ void __launch_bounds__(256) upsample_add_nhwc_kernel(
+    const T* __restrict__ coarse, const T* __restrict__ lat, T* __restrict__ out, int N, int C,
+    int Hc, int Wc, int H, int W, float sy_scale, float sx_scale, int ac) {
+  constexpr int V = kVec ? Vec16<T>::kN : 1;
+  const int cv_per_pix = C / V;
+  const long long total = static_cast<long long>(N) * H * W * cv_per_pix;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int cv = static_cast<int>(i % cv_per_pix);
+    const long long pix = i / cv_per_pix;
+    const int x = static_cast<int>(pix % W);
+    const long long t = pix / W;
+    const int y = static_cast<int>(t % H);
+    const int n = static_cast<int>(t / H);
+    const BilinearTap tp = make_tap(y, x, Hc, Wc, H, W, sy_scale, sx_scale, ac);
+    const size_t cbase = static_cast<size_t>(n) * Hc * Wc;
+    const size_t i00 = (cbase + static_cast<size_t>(tp.y0) * Wc + tp.x0) * C + cv * V;
+    const size_t i01 = (cbase + static_cast<size_t>(tp.y0) * Wc + tp.x1) * C + cv * V;
+    const size_t i10 = (cbase + static_cast<size_t>(tp.y1) * Wc + tp.x0) * C + cv * V;
+    const size_t i11 = (cbase + static_cast<size_t>(tp.y1) * Wc + tp.x1) * C + cv * V;
+    const size_t io = static_cast<size_t>(pix) * C + cv * V;
+    if constexpr (kVec) {
+      Vec16<T> a, b, c, d, l, o;
+      a.u = __ldg(reinterpret_cast<const uint4*>(coarse + i00));
+      b.u = __ldg(reinterpret_cast<const uint4*>(coarse + i01));
+      c.u = __ldg(reinterpret_cast<const uint4*>(coarse + i10));
+      d.u = __ldg(reinterpret_cast<const uint4*>(coarse + i11));
+      if (lat) l.u = __ldg(reinterpret_cast<const uint4*>(lat + io));
+#pragma unroll
+      for (int e = 0; e < V; ++e) {
+        float r = to_f(a.e[e]) * tp.w00 + to_f(b.e[e]) * tp.w01 + to_f(c.e[e]) * tp.w10 +
+                  to_f(d.e[e]) * tp.w11;
+        if (lat) r += to_f(l.e[e]);
+        o.e[e] = from_f<T>(r);
+      }
+      *reinterpret_cast<uint4*>(out + io) = o.u;
+    } else {
+      float r = to_f(coarse[i00]) * tp.w00 + to_f(coarse[i01]) * tp.w01 +
+                to_f(coarse[i10]) * tp.w10 + to_f(coarse[i11]) * tp.w11;
+      if (lat) r += to_f(lat[io]);
+      out[io] = from_f<T>(r);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- NCHW upsample-add
+// One thread per output element; consecutive threads walk x of one plane.
+template <typename T>
+__global__ void __launch_bounds__(256) upsample_add_nchw_kernel(
+    const T* __restrict__ coarse, const T* __restrict__ lat, T* __restrict__ out, int N, int C,
+    int Hc, int Wc, int H, int W, float sy_scale, float sx_scale, int ac) {
+  const long long total = static_cast<long long>(N) * C * H * W;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int x = static_cast<int>(i % W);
+    const long long t = i / W;
+    const int y = static_cast<int>(t % H);
+    const long long plane = t / H;  // n*C + c
+    const BilinearTap tp = make_tap(y, x, Hc, Wc, H, W, sy_scale, sx_scale, ac);
+    const T* cp = coarse + static_cast<size_t>(plane) * Hc * Wc;
+    float r = to_f(__ldg(cp + tp.y0 * Wc + tp.x0)) * tp.w00 +
+              to_f(__ldg(cp + tp.y0 * Wc + tp.x1)) * tp.w01 +
+              to_f(__ldg(cp + tp.y1 * Wc + tp.x0)) * tp.w10 +
+              to_f(__ldg(cp + tp.y1 * Wc + tp.x1)) * tp.w11;
+    if (lat) r += to_f(lat[i]);
+    out[i] = from_f<T>(r);
+  }
+}
+
+// ---------------------------------------------------------------- P6
+// P6 = max_pool2d(P5, kernel=1, stride=2): a single-element window, i.e. P5[::2, ::2].
+template <typename T, bool kVec>
+__global__ void __launch_bounds__(256) p6_nhwc_kernel(const T* __restrict__ in,
+                                                      T* __restrict__ out, int N, int C, int H,
+                                                      int W, int H6, int W6) {
+  constexpr int V = kVec ? Vec16<T>::kN : 1;
+  const int cv_per_pix = C / V;
+  const long long total = static_cast<long long>(N) * H6 * W6 * cv_per_pix;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int cv = static_cast<int>(i % cv_per_pix);
+    const long long pix = i / cv_per_pix;
+    const int x = static_cast<int>(pix % W6);
+    const long long t = pix / W6;
+    const int y = static_cast<int>(t % H6);
+    const int n = static_cast<int>(t / H6);
+    const size_t src = ((static_cast<size_t>(n) * H + 2 * y) * W + 2 * x) * C + cv * V;
+    const size_t dst = static_cast<size_t>(pix) * C + cv * V;
+    if constexpr (kVec) {
+      *reinterpret_cast<uint4*>(out + dst) = __ldg(reinterpret_cast<const uint4*>(in + src));
+    } else {
+      out[dst] = in[src];
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) p6_nchw_kernel(const T* __restrict__ in,
+                                                      T* __restrict__ out, int N, int C, int H,
+                                                      int W, int H6, int W6) {
+  const long long total = static_cast<long long>(N) * C * H6 * W6;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int x = static_cast<int>(i % W6);
+    const long long t = i / W6;
+    const int y = static_cast<int>(t % H6);
+    const long long plane = t / H6;
+    out[i] = in[(static_cast<size_t>(plane) * H + 2 * y) * W + 2 * x];
+  }
+}
+
+// ---------------------------------------------------------------- layout conversion
+// NCHW -> NHWC through a 32x32 shared-memory tile (both sides coalesced).
+template <typename T>
+__global__ void __launch_bounds__(256) nchw_to_nhwc_kernel(const T* __restrict__ in,
+                                                           T* __restrict__ out, int C, int HW) {
+  __shared__ T tile[32][33];
+  const int n = blockIdx.z;
+  const int c0 = blockIdx.y * 32;
+  const int p0 = blockIdx.x * 32;
+  const T* src = in + static_cast<size_t>(n) * C * HW;
+  T* dst = out + static_cast<size_t>(n) * C * HW;
+  for (int r = threadIdx.y; r < 32; r += 8) {
+    const int c = c0 + r, p = p0 + threadIdx.x;
+    if (c < C && p < HW) tile[r][threadIdx.x] = src[static_cast<size_t>(c) * HW + p];
+  }
+  __syncthreads();
+  for (int r = threadIdx.y; r < 32; r += 8) {
+    const int p = p0 + r, c = c0 + threadIdx.x;
+    if (c < C && p < HW) dst[static_cast<size_t>(p) * C + c] = tile[threadIdx.x][r];
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) nhwc_to_nchw_kernel(const T* __restrict__ in,
+                                                           T* __restrict__ out, int C, int HW) {
+  __shared__ T tile[32][33];
+  const int n = blockIdx.z;
+  const int c0 = blockIdx.y * 32;
+  const int p0 = blockIdx.x * 32;
+  const T* src = in + static_cast<size_t>(n) * C * HW;
+  T* dst = out + static_cast<size_t>(n) * C * HW;
+  for (int r = threadIdx.y; r < 32; r += 8) {
+    const int p = p0 + r, c = c0 + threadIdx.x;
+    if (c < C && p < HW) tile[r][threadIdx.x] = src[static_cast<size_t>(p) * C + c];
+  }
+  __syncthreads();
+  for (int r = threadIdx.y; r < 32; r += 8) {
+    const int c = c0 + r, p = p0 + threadIdx.x;
+    if (c < C && p < HW) dst[static_cast<size_t>(c) * HW + p] = tile[threadIdx.x][r];
+  }
+}
+
+// ---------------------------------------------------------------- weight packing
+template <typename T>
+__global__ void convert_kernel(const float* __restrict__ in, T* __restrict__ out, long long n) {
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x)
+    out[i] = from_f<T>(in[i]);
+}
+
+// [Cout][Cin][3][3] fp32 -> [Cout][9][Cin] T (K index = tap * Cin + c, K-major rows).
+template <typename T>
+__global__ void pack_conv3x3_kernel(const float* __restrict__ in, T* __restrict__ out, int Cout,
+                                    int Cin) {
+  const long long total = static_cast<long long>(Cout) * Cin * 9;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(i % Cin);
+    const long long t = i / Cin;
+    const int tap = static_cast<int>(t % 9);
+    const int o = static_cast<int>(t / 9);
+    out[i] = from_f<T>(in[(static_cast<size_t>(o) * Cin + c) * 9 + tap]);
+  }
+}
+
+// ---------------------------------------------------------------- fp32 CUDA-core GEMMs
+// out[n, o, p] = sum_k Wt[o, k] * B(n, k, p) + bias[o] (+ bilinear(coarse)[n, o, p])
+// with B either the NCHW input itself (1x1 conv, k = c) or its on-the-fly
+// im2col (3x3 pad-1 conv, k = c*9 + ky*3 + kx, Wt in natural [Cout][Cin][3][3]).
+// 64x64 output tile per CTA, 256 threads, 4x4 register block, K step 16.
+constexpr int kSB = 64;
+constexpr int kSK = 16;
+
+template <bool kIm2col>
+__global__ void __launch_bounds__(256) fp32_conv_gemm_kernel(
+    const float* __restrict__ x, const float* __restrict__ wt, const float* __restrict__ bias,
+    const float* __restrict__ coarse, float* __restrict__ out, int Cin, int Cout, int H, int W,
+    int Hc, int Wc, float sy_scale, float sx_scale) {
+  __shared__ float sA[kSK][kSB + 4];  // [k][o]
+  __shared__ float sB[kSK][kSB + 4];  // [k][p]
+  const int HW = H * W;
+  const int n = blockIdx.z;
+  const int o0 = blockIdx.y * kSB;
+  const int p0 = blockIdx.x * kSB;
+  const int K = kIm2col ? Cin * 9 : Cin;
+  const float* xn = x + static_cast<size_t>(n) * Cin * HW;
+  const int tx = threadIdx.x & 15;  // pixel group
+  const int ty = threadIdx.x >> 4;  // out-channel group
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += kSK) {
+    // A tile: 64 out x 16 k (4 loads per thread)
+    for (int i = threadIdx.x; i < kSB * kSK; i += 256) {
+      const int kk = i % kSK, oo = i / kSK;
+      const int o = o0 + oo, k = k0 + kk;
+      sA[kk][oo] = (o < Cout && k < K) ? __ldg(wt + static_cast<size_t>(o) * K + k) : 0.f;
+    }
+    // B tile: 16 k x 64 pixels
+    for (int i = threadIdx.x; i < kSB * kSK; i += 256) {
+      const int pp = i % kSB, kk = i / kSB;
+      const int p = p0 + pp, k = k0 + kk;
+      float v = 0.f;
+      if (p < HW && k < K) {
+        if constexpr (kIm2col) {
+          const int c = k / 9, tap = k - c * 9;
+          const int yy = p / W + tap / 3 - 1, xx = p % W + tap % 3 - 1;
+          if (yy >= 0 && yy < H && xx >= 0 && xx < W)
+            v = __ldg(xn + static_cast<size_t>(c) * HW + yy * W + xx);
+        } else {
+          v = __ldg(xn + static_cast<size_t>(k) * HW + p);
+        }
+      }
+      sB[kk][pp] = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < kSK; ++kk) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = sA[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = sB[kk][tx + 16 * j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int o = o0 + ty * 4 + i;
+    if (o >= Cout) continue;
+    const float bo = bias ? __ldg(bias + o) : 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int p = p0 + tx + 16 * j;
+      if (p >= HW) continue;
+      float r = acc[i][j] + bo;
+      if (coarse) {
+        const int y = p / W, xq = p % W;
+        const BilinearTap tp = make_tap(y, xq, Hc, Wc, H, W, sy_scale, sx_scale, 0);
+        const float* cp = coarse + (static_cast<size_t>(n) * Cout + o) * Hc * Wc;
+        r += __ldg(cp + tp.y0 * Wc + tp.x0) * tp.w00 + __ldg(cp + tp.y0 * Wc + tp.x1) * tp.w01 +
+             __ldg(cp + tp.y1 * Wc + tp.x0) * tp.w10 + __ldg(cp + tp.y1 * Wc + tp.x1) * tp.w11;
+      }
+      out[(static_cast<size_t>(n) * Cout + o) * HW + p] = r;
+    }
+  }
+}
+
+int grid_for(long long work, int threads) {
+  long long g = (work + threads - 1) / threads;
+  const long long cap = 148LL * 16;
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return static_cast<int>(g);
+}
+
+template <typename T>
+cudaError_t upsample_add_t(const void* coarse, const void* lat, void* out, int N, int C, int Hc,
+                           int Wc, int H, int W, int ac, Layout layout, cudaStream_t s) {
+  const float sy = (ac && H > 1) ? static_cast<float>(Hc - 1) / (H - 1)
+                                 : static_cast<float>(Hc) / H;
+  const float sx = (ac && W > 1) ? static_cast<float>(Wc - 1) / (W - 1)
+                                 : static_cast<float>(Wc) / W;
+  const T* c = static_cast<const T*>(coarse);
+  const T* l = static_cast<const T*>(lat);
+  T* o = static_cast<T*>(out);
+  if (layout == Layout::NHWC) {
+    constexpr int V = Vec16<T>::kN;
+    const bool vec = (C % V == 0) && aligned16(coarse) && aligned16(out) &&
+                     (lat == nullptr || aligned16(lat));
+    const long long work = static_cast<long long>(N) * H * W * (vec ? C / V : C);
+    if (vec)
+      upsample_add_nhwc_kernel<T, true>
+          <<<grid_for(work, 256), 256, 0, s>>>(c, l, o, N, C, Hc, Wc, H, W, sy, sx, ac);
+    else
+      upsample_add_nhwc_kernel<T, false>
+          <<<grid_for(work, 256), 256, 0, s>>>(c, l, o, N, C, Hc, Wc, H, W, sy, sx, ac);
+  } else {
+    const long long work = static_cast<long long>(N) * C * H * W;
+    upsample_add_nchw_kernel<T>
+        <<<grid_for(work, 256), 256, 0, s>>>(c, l, o, N, C, Hc, Wc, H, W, sy, sx, ac);
+  }
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t p6_t(const void* in, void* out, int N, int C, int H, int W, Layout layout,
+                 cudaStream_t s) {
+  const int H6 = (H - 1) / 2 + 1, W6 = (W - 1) / 2 + 1;
+  const T* i = static_cast<const T*>(in);
+  T* o = static_cast<T*>(out);
+  if (layout == Layout::NHWC) {
+    constexpr int V = Vec16<T>::kN;
+    const bool vec = (C % V == 0) && aligned16(in) && aligned16(out);
+    const long long work = static_cast<long long>(N) * H6 * W6 * (vec ? C / V : C);
+    if (vec)
+      p6_nhwc_kernel<T, true><<<grid_for(work, 256), 256, 0, s>>>(i, o, N, C, H, W, H6, W6);
+    else
+      p6_nhwc_kernel<T, false><<<grid_for(work, 256), 256, 0, s>>>(i, o, N, C, H, W, H6, W6);
+  } else {
+    const long long work = static_cast<long long>(N) * C * H6 * W6;
+    p6_nchw_kernel<T><<<grid_for(work, 256), 256, 0, s>>>(i, o, N, C, H, W, H6, W6);
+  }
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t transpose_t(const void* in, void* out, int N, int C, int HW, bool to_nhwc,
+                        cudaStream_t s) {
+  dim3 grid((HW + 31) / 32, (C + 31) / 32, N), block(32, 8);
+  if (to_nhwc)
+    nchw_to_nhwc_kernel<T>
+        <<<grid, block, 0, s>>>(static_cast<const T*>(in), static_cast<T*>(out), C, HW);
+  else
+    nhwc_to_nchw_kernel<T>
+        <<<grid, block, 0, s>>>(static_cast<const T*>(in), static_cast<T*>(out), C, HW);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_upsample_add(DType dt, const void* coarse, const void* lat, void* out, int N,
+                                int C, int Hc, int Wc, int H, int W, int align_corners,
+                                Layout layout, cudaStream_t s) {
+  switch (dt) {
+    case DType::F32:
+      return upsample_add_t<float>(coarse, lat, out, N, C, Hc, Wc, H, W, align_corners, layout, s);
+    case DType::F16:
+      return upsample_add_t<__half>(coarse, lat, out, N, C, Hc, Wc, H, W, align_corners, layout,
+                                    s);
+    case DType::BF16:
+      return upsample_add_t<__nv_bfloat16>(coarse, lat, out, N, C, Hc, Wc, H, W, align_corners,
+                                           layout, s);
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_p6(DType dt, const void* in, void* out, int N, int C, int H, int W,
+                      Layout layout, cudaStream_t s) {
+  switch (dt) {
+    case DType::F32:
+      return p6_t<float>(in, out, N, C, H, W, layout, s);
+    case DType::F16:
+      return p6_t<__half>(in, out, N, C, H, W, layout, s);
+    case DType::BF16:
+      return p6_t<__nv_bfloat16>(in, out, N, C, H, W, layout, s);
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_transpose(DType dt, const void* in, void* out, int N, int C, int HW,
+                             bool to_nhwc, cudaStream_t s) {
+  switch (dt) {
+    case DType::F32:
+      return transpose_t<float>(in, out, N, C, HW, to_nhwc, s);
+    case DType::F16:
+      return transpose_t<__half>(in, out, N, C, HW, to_nhwc, s);
+    case DType::BF16:
+      return transpose_t<__nv_bfloat16>(in, out, N, C, HW, to_nhwc, s);
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_convert_weights(DType dt, const float* in, void* out, long long n,
+                                   cudaStream_t s) {
+  const int g = grid_for(n, 256);
+  switch (dt) {
+    case DType::F32:
+      return cudaMemcpyAsync(out, in, n * sizeof(float), cudaMemcpyDeviceToDevice, s);
+    case DType::F16:
+      convert_kernel<__half><<<g, 256, 0, s>>>(in, static_cast<__half*>(out), n);
+      break;
+    case DType::BF16:
+      convert_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(in, static_cast<__nv_bfloat16*>(out), n);
+      break;
+    default:
+      return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pack_conv3x3(DType dt, const float* in, void* out, int Cout, int Cin,
+                                cudaStream_t s) {
+  const int g = grid_for(static_cast<long long>(Cout) * Cin * 9, 256);
+  switch (dt) {
+    case DType::F16:
+      pack_conv3x3_kernel<__half><<<g, 256, 0, s>>>(in, static_cast<__half*>(out), Cout, Cin);
+      break;
+    case DType::BF16:
+      pack_conv3x3_kernel<__nv_bfloat16>
+          <<<g, 256, 0, s>>>(in, static_cast<__nv_bfloat16*>(out), Cout, Cin);
+      break;
+    default:
+      return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_fp32_lateral(const float* x, const float* w, const float* bias,
+                                const float* coarse, float* out, int N, int Cin, int Cout, int H,
+                                int W, int Hc, int Wc, cudaStream_t s) {
+  dim3 grid((H * W + kSB - 1) / kSB, (Cout + kSB - 1) / kSB, N);
+  const float sy = coarse ? static_cast<float>(Hc) / H : 0.f;
+  const float sx = coarse ? static_cast<float>(Wc) / W : 0.f;
+  fp32_conv_gemm_kernel<false>
+      <<<grid, 256, 0, s>>>(x, w, bias, coarse, out, Cin, Cout, H, W, Hc, Wc, sy, sx);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_fp32_conv3x3(const float* x, const float* w, const float* bias, float* out,
+                                int N, int Cin, int Cout, int H, int W, cudaStream_t s) {
+  dim3 grid((H * W + kSB - 1) / kSB, (Cout + kSB - 1) / kSB, N);
+  fp32_conv_gemm_kernel<true>
+      <<<grid, 256, 0, s>>>(x, w, bias, nullptr, out, Cin, Cout, H, W, 1, 1, 0.f, 0.f);
+  return cudaGetLastError();
+}
+
+}  // namespace ufpn

@@ -1,0 +1,22 @@
+"""unified_fpn: B200-native FPN neck (lateral 1x1 -> top-down bilinear upsample-add
+-> 3x3 output conv, plus P6), a drop-in for the reference package's public API
+(python/__init__.py:47-59 of sanowl/-UnifiedFPN): ``UnifiedFPN``,
+``fpn_lateral_conv``, ``fpn_upsample_bilinear``, ``fpn_forward_pytorch``,
+``benchmark_fpn``, ``profile_fpn``, ``get_device_info``, ``check_installation``.
+
+The compute runs in libunified_fpn_b200.so (hand-written sm_100a kernels).  If
+that library cannot be loaded the import fails: there is no CPU fallback.
+"""
+from ._lib import UFPNError, lib  # noqa: F401  (raises ImportError without the library)
+from .core import UnifiedFPN, fpn_forward_pytorch
+from .ops import (device_status, fpn_conv3x3, fpn_lateral_conv, fpn_p6, fpn_upsample_add,
+                  fpn_upsample_bilinear, pack_conv3x3_weight)
+from .helpers import benchmark_fpn, check_installation, get_device_info, profile_fpn
+
+__version__ = "1.0.0"
+
+__all__ = [
+    "UnifiedFPN", "fpn_lateral_conv", "fpn_upsample_bilinear", "fpn_forward_pytorch",
+    "fpn_upsample_add", "fpn_p6", "fpn_conv3x3", "pack_conv3x3_weight", "device_status",
+    "benchmark_fpn", "profile_fpn", "get_device_info", "check_installation", "UFPNError",
+]

@@ -1,0 +1,275 @@
+"""``UnifiedFPN``: the FPN neck module (drop-in for the reference's extension class).
+
+Reference: class PyTorchFPNWrapper bound as ``UnifiedFPN`` in python/fpn_pytorch.cpp:9-393
+(constructor ``UnifiedFPN(output_channels=256, workspace_size_mb=512)`` and methods
+forward / initialize_weights / benchmark / get_performance_breakdown / set_kernel_config /
+get_memory_usage), driving class UnifiedFPNCore (lib/core/fpn_engine.cu).
+
+Differences from the reference (whose sources do not build as shipped):
+  * forward takes C2..C5 (a fifth tensor C6 is accepted and ignored) in float32,
+    float16 or bfloat16, NCHW-contiguous or channels_last, and returns P2..P5
+    (plus P6 = max_pool2d(P5, 1, 2) with ``return_p6=True``).  Outputs keep the
+    inputs' memory format.
+  * The neck is the standard one: lateral 1x1 + bias, top-down bilinear
+    upsample (align_corners=False) + add, full 3x3 output conv + bias.
+  * Weights left uninitialised are filled deterministically (Kaiming-normal,
+    fan_in, zero bias, seed 0) instead of from std::random_device.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import Sequence
+
+import torch
+
+from . import _lib
+from ._lib import check, lib
+from .ops import _DT, _stream
+
+_ACT = {"none": 0, "relu": 1, "leaky_relu": 2, "swish": 3}
+
+
+def _ptr_array(ptrs):
+    arr = (ctypes.c_void_p * len(ptrs))()
+    for i, p in enumerate(ptrs):
+        arr[i] = p
+    return arr
+
+
+class UnifiedFPN:
+    """FPN neck on one CUDA device."""
+
+    def __init__(self, output_channels: int = 256, workspace_size_mb: int = 512, device=None):
+        if output_channels != 256:
+            raise ValueError("output_channels must be 256 (the tensor-core tile width)")
+        self.output_channels = output_channels
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        h = ctypes.c_void_p()
+        check(lib.ufpn_core_create(self.device.index or 0, workspace_size_mb << 20, ctypes.byref(h)),
+              "ufpn_core_create")
+        self._h = h
+        self._channels = None       # Cin of C2..C5 the weights were allocated for
+        self._weights_ready = False
+        self._weight_refs = []      # keeps host/device weight tensors alive until copied
+        self._config = None
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            lib.ufpn_core_destroy(h)
+            self._h = None
+
+    # ------------------------------------------------------------------ weights
+    def initialize_weights(self, lateral_weights: Sequence[torch.Tensor], lateral_bias: Sequence[torch.Tensor],
+                           output_weights: Sequence[torch.Tensor], output_bias: Sequence[torch.Tensor]) -> None:
+        """Set the neck's fp32 weights (reference: fpn_pytorch.cpp:24-81).
+
+        lateral_weights[l]: [256, Cin_l] or [256, Cin_l, 1, 1]; lateral_bias[l]: [256];
+        output_weights[l]: [256, 256, 3, 3]; output_bias[l]: [256]; l = 0..3 for P2..P5.
+        CPU or CUDA tensors; they are copied (and packed to the compute dtype) here.
+        """
+        for name, seq in (("lateral_weights", lateral_weights), ("lateral_bias", lateral_bias),
+                          ("output_weights", output_weights), ("output_bias", output_bias)):
+            if len(seq) != 4:
+                raise ValueError(f"Expected 4 weight tensors for each type (P2-P5): {name}")
+        chans = []
+        for l in range(4):
+            lw = lateral_weights[l]
+            if lw.dim() not in (2, 4) or (lw.dim() == 4 and tuple(lw.shape[2:]) != (1, 1)):
+                raise ValueError("Lateral weights must be [out_channels, in_channels] (or [out, in, 1, 1])")
+            if lw.shape[0] != self.output_channels:
+                raise ValueError("Lateral weight output channels must match FPN output channels")
+            if tuple(output_weights[l].shape) != (256, 256, 3, 3):
+                raise ValueError("Output weights must be [256, 256, 3, 3]")
+            if lateral_bias[l].numel() != 256 or output_bias[l].numel() != 256:
+                raise ValueError("biases must have 256 elements")
+            chans.append(int(lw.shape[1]))
+        if chans != self._channels:
+            arr = (ctypes.c_int * 4)(*chans)
+            check(lib.ufpn_core_allocate_weights(self._h, arr, self.output_channels), "allocate_weights")
+            self._channels = chans
+        for l in range(4):
+            ts = [t.detach().to(torch.float32).contiguous() for t in
+                  (lateral_weights[l], lateral_bias[l], output_weights[l], output_bias[l])]
+            if any(t.is_cuda and t.device != self.device for t in ts):
+                ts = [t.to(self.device) for t in ts]
+            if any(t.is_cuda for t in ts):
+                # the engine copies on its own stream: finish the producers first
+                torch.cuda.current_stream(self.device).synchronize()
+            check(lib.ufpn_core_set_weights(self._h, l, *[t.data_ptr() for t in ts]), "set_weights")
+        self._weights_ready = True
+
+    def _default_weights(self, chans):
+        g = torch.Generator().manual_seed(0)
+        lw, lb, ow, ob = [], [], [], []
+        for cin in chans:
+            lw.append(torch.randn(256, cin, generator=g) * math.sqrt(2.0 / cin))
+            lb.append(torch.zeros(256))
+            ow.append(torch.randn(256, 256, 3, 3, generator=g) * math.sqrt(2.0 / (256 * 9)))
+            ob.append(torch.zeros(256))
+        self.initialize_weights(lw, lb, ow, ob)
+
+    # ------------------------------------------------------------------ forward
+    def _configure(self, feats):
+        x0 = feats[0]
+        if x0.dtype not in _DT:
+            raise TypeError("inputs must be float32, float16 or bfloat16")
+        for t in feats:
+            if not t.is_cuda or t.device != self.device:
+                raise ValueError("All input tensors must be on the engine's CUDA device")
+            if t.dim() != 4:
+                raise ValueError("All input tensors must be 4D [N, C, H, W]")
+            if t.dtype != x0.dtype:
+                raise ValueError("All input tensors must share one dtype")
+            if t.shape[0] != x0.shape[0]:
+                raise ValueError("All input tensors must share the batch size")
+        if x0.dtype != torch.float32 and all(
+                t.is_contiguous(memory_format=torch.channels_last) for t in feats):
+            layout = _lib.LAYOUT_NHWC
+        else:
+            layout = _lib.LAYOUT_NCHW
+        chans = [int(t.shape[1]) for t in feats]
+        cfg = (tuple(tuple(t.shape) for t in feats), x0.dtype, layout)
+        if cfg != self._config:
+            N = int(x0.shape[0])
+            ci = (ctypes.c_int * 4)(*chans)
+            hi = (ctypes.c_int * 4)(*[int(t.shape[2]) for t in feats])
+            wi = (ctypes.c_int * 4)(*[int(t.shape[3]) for t in feats])
+            check(lib.ufpn_core_configure_levels(self._h, N, ci, hi, wi, self.output_channels,
+                                                 _DT[x0.dtype], layout), "configure_levels")
+            self._config = cfg
+        if not self._weights_ready or chans != self._channels:
+            if self._weights_ready:
+                raise ValueError(f"weights were initialised for input channels {self._channels}, got {chans}")
+            self._default_weights(chans)
+        return layout
+
+    def _prepare(self, backbone_features):
+        if len(backbone_features) not in (4, 5):
+            raise ValueError("Expected C2..C5 (or C2..C6) backbone feature tensors")
+        feats = list(backbone_features[:4])
+        layout = self._configure(feats)
+        mf = torch.channels_last if layout == _lib.LAYOUT_NHWC else torch.contiguous_format
+        feats = [t.contiguous(memory_format=mf) for t in feats]
+        return feats, layout, mf
+
+    def _alloc_outputs(self, feats, mf, return_p6):
+        N = feats[0].shape[0]
+        outs = [torch.empty((N, 256, t.shape[2], t.shape[3]), dtype=t.dtype, device=t.device, memory_format=mf)
+                for t in feats]
+        p6 = None
+        if return_p6:
+            H5, W5 = feats[3].shape[2], feats[3].shape[3]
+            p6 = torch.empty((N, 256, (H5 - 1) // 2 + 1, (W5 - 1) // 2 + 1), dtype=feats[0].dtype,
+                             device=feats[0].device, memory_format=mf)
+        return outs, p6
+
+    def forward(self, backbone_features: Sequence[torch.Tensor], return_p6: bool = False,
+                out: Sequence[torch.Tensor] | None = None):
+        """P2..P5 (and P6) of the neck; stream-ordered on torch's current stream."""
+        feats, layout, mf = self._prepare(backbone_features)
+        if out is not None:
+            outs = list(out[:4])
+            p6 = out[4] if (return_p6 and len(out) > 4) else None
+            if return_p6 and p6 is None:
+                raise ValueError("out must hold 5 tensors when return_p6=True")
+        else:
+            outs, p6 = self._alloc_outputs(feats, mf, return_p6)
+        ins = _ptr_array([t.data_ptr() for t in feats])
+        os_ = _ptr_array([t.data_ptr() for t in outs])
+        check(lib.ufpn_core_forward(self._h, ins, os_, p6.data_ptr() if p6 is not None else None,
+                                    _stream(feats[0])), "forward")
+        return outs + [p6] if return_p6 else outs
+
+    __call__ = forward
+
+    # ------------------------------------------------------------------ tooling
+    def benchmark(self, backbone_features, num_iterations: int = 100):
+        """(avg_ms, GB/s, compute utilisation) of the neck, timed with CUDA events
+        on the current stream (reference: fpn_pytorch.cpp:139-169 timed with the
+        host clock)."""
+        feats, layout, mf = self._prepare(backbone_features)
+        outs, p6 = self._alloc_outputs(feats, mf, True)
+        out = outs + [p6]
+        for _ in range(10):
+            self.forward(feats, return_p6=True, out=out)
+        s = torch.cuda.current_stream(self.device)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(num_iterations):
+            self.forward(feats, return_p6=True, out=out)
+        e1.record(s)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / num_iterations
+        esz = feats[0].element_size()
+        nbytes = 0.0
+        flops = 0.0
+        for t in feats:
+            px = t.shape[0] * t.shape[2] * t.shape[3]
+            nbytes += px * (t.shape[1] + 256) * esz
+            flops += 2.0 * px * 256 * (t.shape[1] + 9 * 256)
+        peak = 2.25e15 if feats[0].dtype != torch.float32 else 8.0e13
+        return ms, nbytes / (ms * 1e-3) / 1e9, flops / (ms * 1e-3) / peak
+
+    def get_performance_breakdown(self, backbone_features=None):
+        """[kernel_times_ms(8), metrics(5)] as in fpn_pytorch.cpp:171-187.  With
+        ``backbone_features`` given, first runs one profiled (serialised) forward."""
+        if backbone_features is not None:
+            check(lib.ufpn_core_set_profiling(self._h, 1), "set_profiling")
+            self.forward(backbone_features, return_p6=True)
+        kt = (ctypes.c_float * 8)()
+        mt = (ctypes.c_float * 5)()
+        check(lib.ufpn_core_get_performance_metrics(self._h, kt, mt), "get_performance_metrics")
+        return [torch.tensor(list(kt), dtype=torch.float32), torch.tensor(list(mt), dtype=torch.float32)]
+
+    def set_kernel_config(self, tile_size: int = 0, channels_per_thread: int = 8, use_tensor_cores: bool = True,
+                          activation: str = "none", enable_graph_capture: bool = True) -> None:
+        """Reference: fpn_pytorch.cpp:189-209.  tile_size is the 3x3 tile width
+        (8..128; 0 = tuned/heuristic); only activation="none" exists in this neck."""
+        if activation not in _ACT:
+            raise ValueError(f"unknown activation {activation!r}")
+        check(lib.ufpn_core_set_kernel_config(self._h, tile_size, channels_per_thread, int(use_tensor_cores),
+                                              _ACT[activation], int(enable_graph_capture)), "set_kernel_config")
+
+    def get_memory_usage(self) -> int:
+        return int(lib.ufpn_core_get_memory_usage(self._h))
+
+    def autotune(self, backbone_features, iterations: int = 10) -> str:
+        """Times every candidate 3x3 tiling per level and keeps the fastest."""
+        feats, layout, mf = self._prepare(backbone_features)
+        outs, p6 = self._alloc_outputs(feats, mf, True)
+        check(lib.ufpn_core_autotune(self._h, _ptr_array([t.data_ptr() for t in feats]),
+                                     _ptr_array([t.data_ptr() for t in outs]), p6.data_ptr(),
+                                     _stream(feats[0]), iterations), "autotune")
+        return lib.ufpn_last_error().decode()
+
+    def save_tuning(self, path: str) -> None:
+        check(lib.ufpn_core_save_tuning(self._h, str(path).encode()), "save_tuning")
+
+    def load_tuning(self, path: str) -> None:
+        check(lib.ufpn_core_load_tuning(self._h, str(path).encode()), "load_tuning")
+
+    def device_status(self, reset: bool = True) -> int:
+        v = ctypes.c_int(0)
+        check(lib.ufpn_core_device_status(self._h, int(reset), ctypes.byref(v)), "device_status")
+        return v.value
+
+
+_SINGLETON: dict = {}
+
+
+def fpn_forward_pytorch(backbone_features, lateral_weights, output_weights, lateral_bias=None,
+                        output_bias=None):
+    """Whole-neck forward with the given weights (reference: fpn_pytorch.cpp:360-367,
+    which used a static engine and ignored its weight arguments).  Biases default to zero."""
+    dev = backbone_features[0].device
+    key = dev.index
+    fpn = _SINGLETON.get(key)
+    if fpn is None:
+        fpn = _SINGLETON[key] = UnifiedFPN(device=dev)
+    lb = lateral_bias if lateral_bias is not None else [torch.zeros(256) for _ in range(4)]
+    ob = output_bias if output_bias is not None else [torch.zeros(256) for _ in range(4)]
+    fpn.initialize_weights(lateral_weights, lb, output_weights, ob)
+    return fpn.forward(backbone_features)

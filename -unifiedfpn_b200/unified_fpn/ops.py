@@ -1,0 +1,181 @@
+"""Standalone FPN operators over the C ABI (the free functions of the reference's
+extension module, python/fpn_pytorch.cpp:293-367, plus the ops it lacked).
+
+All ops run on the tensors' CUDA device, on torch's current stream, and never
+block the host.  16-bit tensors use the tensor-core / vectorised NHWC kernels
+(channels_last tensors); fp32 tensors use the NCHW CUDA-core kernels.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import check, lib
+
+_DT = {torch.float32: _lib.DTYPE_F32, torch.float16: _lib.DTYPE_F16, torch.bfloat16: _lib.DTYPE_BF16}
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DT[t.dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {t.dtype}: expected float32, float16 or bfloat16") from None
+
+
+def layout_of(t: torch.Tensor) -> int:
+    """NHWC if the 4-D tensor is channels_last-contiguous, NCHW if contiguous."""
+    if t.dim() == 4 and t.is_contiguous(memory_format=torch.channels_last) and not (
+            t.is_contiguous() and t.shape[1] > 1 and t.shape[2] * t.shape[3] > 1):
+        return _lib.LAYOUT_NHWC
+    if t.is_contiguous():
+        return _lib.LAYOUT_NCHW
+    raise ValueError("tensor must be contiguous (NCHW) or channels_last (NHWC)")
+
+
+def _empty_like_layout(shape, ref: torch.Tensor, layout: int, dtype=None) -> torch.Tensor:
+    mf = torch.channels_last if layout == _lib.LAYOUT_NHWC else torch.contiguous_format
+    return torch.empty(shape, dtype=dtype or ref.dtype, device=ref.device, memory_format=mf)
+
+
+def _stream(t: torch.Tensor):
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _check_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("all tensors must be CUDA tensors")
+
+
+def fpn_lateral_conv(input: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor,
+                     coarse: torch.Tensor | None = None) -> torch.Tensor:
+    """1x1 lateral conv + bias, optionally fused with the top-down upsample-add:
+    ``out = conv1x1(input, weight) + bias [+ bilinear_upsample(coarse, input size)]``.
+
+    Reference: fpn_lateral_conv (python/fpn_pytorch.cpp:293-326) ->
+    lateral_conv_kernel (lib/kernels/compute/fpn_compute_kernels.cu:127-230).
+    ``weight`` is [Cout, Cin] or [Cout, Cin, 1, 1]; ``bias`` [Cout] (fp32).
+    fp32 input: NCHW, any Cout.  16-bit input: channels_last, Cout = 256.
+    """
+    _check_cuda(input, weight, bias, coarse)
+    if input.dim() != 4:
+        raise ValueError("input must be 4-D [N, C, H, W]")
+    N, Cin, H, W = input.shape
+    Cout = weight.shape[0]
+    if weight.numel() != Cout * Cin:
+        raise ValueError("weight must be [Cout, Cin] or [Cout, Cin, 1, 1]")
+    dt = dtype_code(input)
+    if dt == _lib.DTYPE_F32:
+        input = input.contiguous()
+        lay = _lib.LAYOUT_NCHW
+    else:
+        input = input.contiguous(memory_format=torch.channels_last)
+        lay = _lib.LAYOUT_NHWC
+    w = weight.reshape(Cout, Cin).to(device=input.device, dtype=input.dtype).contiguous()
+    b = bias.to(device=input.device, dtype=torch.float32).contiguous()
+    Hc = Wc = 0
+    if coarse is not None:
+        if coarse.dtype != input.dtype or coarse.shape[0] != N or coarse.shape[1] != Cout:
+            raise ValueError("coarse must match the output's dtype, batch and channels")
+        coarse = coarse.contiguous(memory_format=torch.channels_last if lay == _lib.LAYOUT_NHWC
+                                   else torch.contiguous_format)
+        Hc, Wc = coarse.shape[2], coarse.shape[3]
+    out = _empty_like_layout((N, Cout, H, W), input, lay)
+    check(lib.ufpn_lateral_conv(dt, lay, input.data_ptr(), w.data_ptr(), b.data_ptr(),
+                                coarse.data_ptr() if coarse is not None else None, out.data_ptr(),
+                                N, Cin, H, W, Cout, Hc, Wc, _stream(input)), "ufpn_lateral_conv")
+    return out
+
+
+def pack_conv3x3_weight(weight: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """[256, 256, 3, 3] fp32 -> [256, 9, 256] (K-major) in ``dtype`` for the tensor-core 3x3."""
+    Cout, Cin = weight.shape[0], weight.shape[1]
+    w32 = weight.to(dtype=torch.float32).contiguous()
+    out = torch.empty((Cout, 9, Cin), dtype=dtype, device=weight.device)
+    check(lib.ufpn_pack_conv3x3_weights(_DT[dtype], w32.data_ptr(), out.data_ptr(), Cout, Cin,
+                                        _stream(weight)), "ufpn_pack_conv3x3_weights")
+    return out
+
+
+def fpn_conv3x3(input: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, p6: bool = False,
+                tile_w: int = 0):
+    """3x3 pad-1 output conv (256 -> 256) + bias; with ``p6=True`` also returns
+    P6 = max_pool2d(out, 1, 2).  ``weight`` is [256, 256, 3, 3] (any float dtype)
+    or, for 16-bit inputs, already packed [256, 9, 256] by :func:`pack_conv3x3_weight`.
+    """
+    _check_cuda(input, weight, bias)
+    N, C, H, W = input.shape
+    if C != 256:
+        raise ValueError("the output conv maps 256 -> 256 channels")
+    dt = dtype_code(input)
+    if dt == _lib.DTYPE_F32:
+        x = input.contiguous()
+        w = weight.to(torch.float32).contiguous()
+        lay = _lib.LAYOUT_NCHW
+    else:
+        x = input.contiguous(memory_format=torch.channels_last)
+        w = weight if (weight.dim() == 3 and weight.dtype == input.dtype) else pack_conv3x3_weight(
+            weight, input.dtype)
+        lay = _lib.LAYOUT_NHWC
+    b = bias.to(device=input.device, dtype=torch.float32).contiguous()
+    out = _empty_like_layout((N, 256, H, W), x, lay)
+    p6t = _empty_like_layout((N, 256, (H - 1) // 2 + 1, (W - 1) // 2 + 1), x, lay) if p6 else None
+    check(lib.ufpn_conv3x3(dt, x.data_ptr(), w.data_ptr(), b.data_ptr(), out.data_ptr(),
+                           p6t.data_ptr() if p6t is not None else None, N, H, W, tile_w,
+                           _stream(x)), "ufpn_conv3x3")
+    return (out, p6t) if p6 else out
+
+
+def fpn_upsample_add(coarse: torch.Tensor, lateral: torch.Tensor | None = None,
+                     size: tuple[int, int] | None = None, align_corners: bool = False) -> torch.Tensor:
+    """``lateral + bilinear_upsample(coarse, lateral's H x W)`` (or a pure upsample to
+    ``size`` when ``lateral`` is None).  Reference: launch_upsample_and_add
+    (lib/core/fpn_engine.cu:274-313)."""
+    _check_cuda(coarse, lateral)
+    dt = dtype_code(coarse)
+    lay = layout_of(coarse)
+    N, C, Hc, Wc = coarse.shape
+    if lateral is not None:
+        if lateral.dtype != coarse.dtype or lateral.shape[:2] != coarse.shape[:2]:
+            raise ValueError("lateral must match coarse in dtype, batch and channels")
+        H, W = lateral.shape[2], lateral.shape[3]
+        lateral = lateral.contiguous(memory_format=torch.channels_last if lay == _lib.LAYOUT_NHWC
+                                     else torch.contiguous_format)
+    else:
+        if size is None:
+            raise ValueError("size is required without a lateral tensor")
+        H, W = size
+    out = _empty_like_layout((N, C, H, W), coarse, lay)
+    check(lib.ufpn_upsample_add(dt, lay, coarse.data_ptr(),
+                                lateral.data_ptr() if lateral is not None else None, out.data_ptr(),
+                                N, C, Hc, Wc, H, W, int(align_corners), _stream(coarse)),
+          "ufpn_upsample_add")
+    return out
+
+
+def fpn_upsample_bilinear(input: torch.Tensor, scale_factor: float) -> torch.Tensor:
+    """Bilinear upsample by ``scale_factor``; output size = int(in * scale), sampled
+    with scale = in / out (half-pixel, align_corners=False).
+    Reference: fpn_upsample_bilinear (python/fpn_pytorch.cpp:328-358)."""
+    H = int(input.shape[2] * scale_factor)
+    W = int(input.shape[3] * scale_factor)
+    return fpn_upsample_add(input, None, size=(H, W))
+
+
+def fpn_p6(p5: torch.Tensor) -> torch.Tensor:
+    """P6 = max_pool2d(P5, kernel_size=1, stride=2)."""
+    _check_cuda(p5)
+    dt = dtype_code(p5)
+    lay = layout_of(p5)
+    N, C, H, W = p5.shape
+    out = _empty_like_layout((N, C, (H - 1) // 2 + 1, (W - 1) // 2 + 1), p5, lay)
+    check(lib.ufpn_p6_maxpool(dt, lay, p5.data_ptr(), out.data_ptr(), N, C, H, W, _stream(p5)),
+          "ufpn_p6_maxpool")
+    return out
+
+
+def device_status(reset: bool = True) -> int:
+    """Status word of the standalone tensor-core ops on the current device (0 = ok)."""
+    v = _lib.c_int(0)
+    check(lib.ufpn_device_status(int(reset), _lib.ctypes.byref(v)), "ufpn_device_status")
+    return v.value

@@ -1,0 +1,380 @@
+"""Benchmark: FPN-neck images/s on B200 (R50 800x1216, bf16, batch 2 per GPU).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one forward of the whole neck (4 fused laterals + 4 implicit-GEMM 3x3
+convs + P6) over one batch.  Multi-GPU (torchrun, one process per GPU): every
+rank runs its own batch slice with no collective on the data path (weak
+scaling); timing is a barrier-bracketed CUDA-event window, max over ranks.
+
+Prints ONE JSON line (rank 0).  Keys beyond the base contract:
+  e2e         same metric through the public API (UnifiedFPN.forward) with the
+              inputs copied from pinned host memory and P2..P6 copied back each step
+  roofline    the dominant kernel (P2 3x3 implicit GEMM) timed live with CUDA events
+  cpu_baseline  the CPU oracle neck (fp32 torch CPU, all host threads) on a bounded sample
+  clocks      nvidia-smi samples taken during the timed window
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "-unifiedfpn_b200"))
+
+import torch  # noqa: E402
+
+METRIC = "FPN-neck images/sec, R50 800×1216 bf16 @1/2/4/8 B200; % of roofline"
+R50_CHANNELS = (256, 512, 1024, 2048)
+
+
+def level_sizes(h, w):
+    return [(-(-h // s), -(-w // s)) for s in (4, 8, 16, 32)]
+
+
+def neck_flops(batch, chans, sizes):
+    f = 0.0
+    for c, (h, w) in zip(chans, sizes):
+        px = batch * h * w
+        f += 2.0 * px * 256 * c + 2.0 * px * 256 * 256 * 9
+    return f
+
+
+def neck_bytes(batch, chans, sizes, esz):
+    """Compulsory HBM bytes: read C2..C5 and weights, write P2..P6."""
+    b = 0.0
+    for c, (h, w) in zip(chans, sizes):
+        px = batch * h * w
+        b += px * (c + 256) * esz + (256 * c + 9 * 256 * 256) * esz
+    h5, w5 = sizes[3]
+    b += batch * ((h5 + 1) // 2) * ((w5 + 1) // 2) * 256 * esz
+    return b
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "src": "fallback"}
+
+
+def profile_traffic(name):
+    """dram bytes per launch from a committed ncu summary (profiles/<name>.txt), else None."""
+    p = ROOT / "profiles" / f"{name}.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("dram_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed window."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.out = None
+
+    def start(self):
+        try:
+            self.out = open(os.devnull, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=self.out, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            text, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            text, _ = self.proc.communicate()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in text.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_baseline(seconds=12.0, image=(800, 1216)):
+    """The CPU oracle neck (fp32, torch CPU, all host threads) on one image per iteration."""
+    from oracle import fpn_oracle as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    sizes = level_sizes(*image)
+    feats = O.make_features(1, R50_CHANNELS, sizes, seed=0)
+    wts = O.make_weights(R50_CHANNELS, seed=1)
+    with torch.no_grad():
+        O.fpn_neck(feats, wts)  # warm-up
+        n, t0 = 0, time.perf_counter()
+        while True:
+            O.fpn_neck(feats, wts)
+            n += 1
+            el = time.perf_counter() - t0
+            if el >= seconds or n >= 50:
+                break
+    return {"value": n / el, "unit": "images/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{n} x 1 image R50 800x1216 fp32 (torch CPU oracle neck, {el:.1f} s)"}
+
+
+def run_reference(args, rank, world):
+    """Reference arm: the reference's CPU path for this neck, i.e. the oracle port
+    (the reference's own host code covers only the bilinear upsample; its neck
+    does not build), on rank 0 with all host threads."""
+    if rank != 0:
+        return 0
+    from oracle import fpn_oracle as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    sizes = level_sizes(args.height, args.width)
+    feats = O.make_features(1, R50_CHANNELS, sizes, seed=0)
+    wts = O.make_weights(R50_CHANNELS, seed=1)
+    with torch.no_grad():
+        for _ in range(max(1, min(args.warmup, 1))):
+            O.fpn_neck(feats, wts)
+        steps = max(1, min(args.steps, 5))
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            O.fpn_neck(feats, wts)
+        el = time.perf_counter() - t0
+    v = steps / el
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "images/s", "n_gpus": world,
+        "steps": steps, "warmup": 1, "ms_per_step": el * 1e3 / steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) after ReLU clamp)",
+        "config": {"workload": f"R50 FPN neck {args.height}x{args.width}, 1 image per step (bounded CPU sample)",
+                   "global_batch": 1, "parallelism": "host threads"},
+        "cpu_baseline": {"value": v, "unit": "images/s", "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": f"{steps} x 1 image R50 {args.height}x{args.width} fp32 torch CPU oracle neck"},
+        "e2e": {"value": v, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=2, help="images per GPU")
+    ap.add_argument("--height", type=int, default=800)
+    ap.add_argument("--width", type=int, default=1216)
+    ap.add_argument("--dtype", choices=["bf16", "fp16"], default="bf16")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-roofline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import torch.distributed as dist
+    from datetime import timedelta
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+
+    import unified_fpn as U
+
+    dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float16
+    esz = 2
+    sizes = level_sizes(args.height, args.width)
+    B = args.batch
+    n_sets = 3  # rotating input sets: 3 x ~117 MB of C2..C5 > 126 MB L2
+    gen = torch.Generator(device=dev)
+    feats = []
+    for s in range(n_sets):
+        gen.manual_seed(1000 * rank + s)
+        feats.append([torch.randn(B, c, h, w, device=dev, generator=gen, dtype=torch.float32).clamp_min_(0)
+                      .to(dtype).contiguous(memory_format=torch.channels_last)
+                      for c, (h, w) in zip(R50_CHANNELS, sizes)])
+    fpn = U.UnifiedFPN(device=dev)
+    outs = []
+    for s in range(n_sets):
+        o = fpn(feats[s], return_p6=True)
+        outs.append(o)
+    torch.cuda.synchronize(dev)
+
+    def step(i):
+        fpn(feats[i % n_sets], return_p6=True, out=outs[i % n_sets])
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize(dev)
+    if fpn.device_status() != 0:
+        raise RuntimeError("device pipeline timeout during warm-up")
+    launches_per_step = int(fpn.get_performance_breakdown()[1][4].item())
+
+    stream = torch.cuda.current_stream(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    clocks.start()
+    time.sleep(0.3)  # let the sampler take its first reading
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    status = fpn.device_status()
+    images = B * world * args.steps
+    value = images / (ms / 1e3)
+    ms_per_step = ms / args.steps
+
+    # ---------------------------------------------------------------- e2e through the public API
+    e2e = None
+    if not args.no_e2e:
+        host_in = [f.cpu().pin_memory() for f in feats[0]]
+        host_out = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs[0]]
+        dev_in = [torch.empty_like(f) for f in feats[0]]
+        h2d = sum(t.numel() * t.element_size() for t in host_in)
+        d2h = sum(t.numel() * t.element_size() for t in host_out)
+
+        def e2e_step():
+            for d, h in zip(dev_in, host_in):
+                d.copy_(h, non_blocking=True)  # NHWC strides are preserved
+            res = fpn(dev_in, return_p6=True, out=outs[0])
+            for h, r in zip(host_out, res):
+                h.copy_(r, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        n_e2e = max(3, min(args.steps, 10))
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        a0 = torch.cuda.Event(enable_timing=True)
+        a1 = torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for _ in range(n_e2e):
+            e2e_step()
+        a1.record(stream)
+        torch.cuda.synchronize(dev)
+        ems = a0.elapsed_time(a1)
+        if world > 1:
+            t = torch.tensor([ems], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = float(t.item())
+        e2e = {"value": B * world * n_e2e / (ems / 1e3), "unit": "images/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "steps": n_e2e}
+
+    # ---------------------------------------------------------------- roofline of the dominant kernel
+    roofline = None
+    peaks = measured_peaks()
+    kernel_share = None
+    if not args.no_roofline:
+        kt, mt = fpn.get_performance_breakdown(feats[0])  # one serialised, event-timed forward
+        total = float(kt.sum().item())
+        kernel_share = {n: round(float(v) / total, 4) for n, v in zip(
+            ["lateral_P5", "conv3x3_P5", "lateral_P4", "conv3x3_P4", "lateral_P3", "conv3x3_P3",
+             "lateral_P2", "conv3x3_P2"], kt.tolist())} if total > 0 else None
+        h2, w2 = sizes[0]
+        x = torch.randn(B, 256, h2, w2, device=dev, generator=gen).to(dtype).contiguous(
+            memory_format=torch.channels_last)
+        wt = U.pack_conv3x3_weight(torch.randn(256, 256, 3, 3, device=dev, generator=gen) * 0.03, dtype)
+        bias = torch.zeros(256, device=dev)
+        reps = 20
+        for _ in range(3):
+            U.fpn_conv3x3(x, wt, bias)
+        r0 = torch.cuda.Event(enable_timing=True)
+        r1 = torch.cuda.Event(enable_timing=True)
+        r0.record(stream)
+        for _ in range(reps):
+            U.fpn_conv3x3(x, wt, bias)
+        r1.record(stream)
+        torch.cuda.synchronize(dev)
+        kms = r0.elapsed_time(r1) / reps
+        flops = 2.0 * B * h2 * w2 * 256 * 256 * 9
+        achieved = flops / (kms * 1e-3) / 1e12
+        traffic = profile_traffic("conv3x3_p2_r50_800x1216_b2")
+        roofline = {"kernel": f"conv3x3 P2 implicit GEMM (tcgen05), {B}x{h2}x{w2}x256 -> 256",
+                    "bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"],
+                    "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
+                    "peak_src": f"{peaks['src']} bf16 burst (kernel timed alone)",
+                    "launch_ms": round(kms, 4), "flops_per_launch": flops, "traffic": traffic,
+                    "neck_frac_of_roofline": None}
+        # whole-neck roofline: slower of FLOPs at the sustained tensor peak and bytes at HBM peak
+        f_all = neck_flops(B, R50_CHANNELS, sizes)
+        b_all = neck_bytes(B, R50_CHANNELS, sizes, esz)
+        t_roof = max(f_all / (peaks["bf16_tflops_sustained"] * 1e12), b_all / (peaks["hbm_gbs"] * 1e9))
+        roofline["neck_frac_of_roofline"] = round(t_roof * 1e3 / ms_per_step, 4)
+        roofline["neck_roofline_ms"] = round(t_roof * 1e3, 4)
+
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline and world == 1:
+        cpu = cpu_baseline()
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "images/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": args.dtype,
+            "data": "synthetic (seeded N(0,1) after ReLU clamp; random Kaiming-normal weights)",
+            "config": {"workload": f"R50 FPN neck {args.height}x{args.width}, {B} images/GPU, {args.dtype} NHWC",
+                       "global_batch": B * world, "per_gpu_batch": B,
+                       "levels": [[B, c, h, w] for c, (h, w) in zip(R50_CHANNELS, sizes)],
+                       "l2": f"inputs rotate over {n_sets} sets (~{n_sets * 117} MB at 800x1216 b2) > 126 MB L2",
+                       "parallelism": f"dp{world} batch shards, no collective on the data path"},
+            "clocks": clk, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
+            "roofline": roofline, "kernel_time_share": kernel_share, "cpu_baseline": cpu,
+            "device_status": status,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,75 @@
+// UnifiedFPNCore: the FPN neck engine (C++ API).
+//
+// Replaces lib/core/fpn_engine.cu:10-416 of the reference with the same method
+// names.  Differences a caller sees:
+//   * forward() is stream-ordered on the caller's stream and never blocks the
+//     host (the reference synchronised four private streams every call,
+//     fpn_engine.cu:239-241).
+//   * The neck computed is the standard one: M5 = lat(C5); M_l = lat(C_l) +
+//     bilinear_up(M_{l+1}); P_l = conv3x3(M_l) (full 256->256 conv, bias, no
+//     BN/ReLU); P6 = max_pool2d(P5, 1, 2).
+//   * Inputs are C2..C5 (a fifth tensor, C6, is accepted and ignored).
+//   * 16-bit inputs run on the tensor cores (tcgen05 + TMA), fp32 inputs on the
+//     CUDA cores in full fp32.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "unified_fpn/core/types.h"
+
+class __attribute__((visibility("default"))) UnifiedFPNCore {
+ public:
+  explicit UnifiedFPNCore(size_t workspace_size = 512ull << 20, int device = -1);
+  ~UnifiedFPNCore();
+  UnifiedFPNCore(const UnifiedFPNCore&) = delete;
+  UnifiedFPNCore& operator=(const UnifiedFPNCore&) = delete;
+
+  // backbone_dims: C2..C5 (4 entries) or C2..C6 (5, the last ignored).
+  // dtype: FLOAT32, FLOAT16 or BFLOAT16.  layout: layout of inputs and outputs.
+  void configure_levels(const std::vector<FPNDimensions>& backbone_dims, int output_channels,
+                        FPNDataType dtype = FPNDataType::FLOAT32,
+                        FPNLayout layout = FPNLayout::NCHW);
+  // backbone_channels: Cin of C2..C5 (4 entries) or the reference's 5-entry form
+  // {unused, C2, C3, C4, C5}.
+  void allocate_weights(const std::vector<int>& backbone_channels, int output_channels);
+  // fp32 weights, host or device memory: lateral [256][Cin] (or [256][Cin][1][1]),
+  // bias [256], output [256][256][3][3], bias [256].
+  void set_weights(int level, const float* lateral_weights, const float* lateral_bias,
+                   const float* output_weights, const float* output_bias);
+
+  // inputs: C2..C5 (or C2..C6); outputs: P2..P5 (4) or P2..P6 (5).
+  template <typename T>
+  void forward(const std::vector<FPNTensor<T>>& backbone_features,
+               std::vector<FPNTensor<T>>& output_features, cudaStream_t stream = nullptr);
+
+  const FPNPerformanceMetrics& get_performance_metrics() const;
+  void set_kernel_config(const FPNKernelConfig& config);
+  size_t get_memory_usage() const;
+
+  // Time every kernel of the next forward() with CUDA events (serialises the
+  // schedule; synchronises the stream at the end of that forward).
+  void set_profiling(bool enable);
+  // Measure the candidate tilings of every level with the given buffers and keep
+  // the fastest; returns a human-readable report.
+  std::string autotune(const void* const* inputs, void* const* outputs, void* p6,
+                       cudaStream_t stream, int iterations = 10);
+  bool save_tuning(const std::string& path) const;
+  bool load_tuning(const std::string& path);
+
+  // Reads (and optionally clears) the device status word the kernels write on a
+  // pipeline timeout.  Synchronises the device.
+  int device_status(bool reset);
+
+  // Untyped entry point used by the C ABI.
+  void forward_raw(const void* const* inputs, void* const* outputs, void* p6,
+                   cudaStream_t stream);
+
+  struct Impl;
+
+ private:
+  std::unique_ptr<Impl> impl_;
+};

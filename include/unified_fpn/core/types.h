@@ -1,0 +1,158 @@
+// Public C++ types of the B200 FPN-neck library.
+//
+// Names, members and meanings follow the reference's public header
+// include/unified_fpn/core/types.h so code written against it keeps compiling:
+//   FPNException / FPN_THROW ............ types.h:24-46
+//   CUDA_CHECK .......................... types.h:140-186 (throws, never exit())
+//   FPNDataType ......................... types.h:208-223 (same ordinal values)
+//   FPNActivation ....................... types.h:295-300
+//   FPNDimensions ....................... types.h:302-308
+//   FPNLevelConfig ...................... types.h:310-315
+//   FPNTensor<T> ........................ types.h:317-333 (+ layout member)
+//   FPNKernelConfig ..................... types.h:335-361 (subset that has meaning here)
+//   FPNWeights .......................... types.h:363-376
+//   FPNPerformanceMetrics ............... types.h:378-405
+// The declared-but-never-defined reference classes (DeviceCapabilities,
+// MemoryPool, AutoTuner, PrecisionConfig) are not carried over; the CUDA
+// caching allocator of the caller and the measured autotuner of the engine
+// (include/unified_fpn/core/engine.h) take their place.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <exception>
+#include <string>
+
+class FPNException : public std::exception {
+ public:
+  FPNException(const std::string& message, const char* file, int line, const char* function)
+      : message_(message), file_(file), line_(line), function_(function) {
+    full_message_ = "FPN Error in " + std::string(function) + " at " + std::string(file) + ":" +
+                    std::to_string(line) + " - " + message;
+  }
+  const char* what() const noexcept override { return full_message_.c_str(); }
+  const std::string& get_message() const { return message_; }
+  const char* get_file() const { return file_; }
+  int get_line() const { return line_; }
+  const char* get_function() const { return function_; }
+
+ private:
+  std::string message_;
+  std::string full_message_;
+  const char* file_;
+  int line_;
+  const char* function_;
+};
+
+#define FPN_THROW(message) throw FPNException(message, __FILE__, __LINE__, __func__)
+
+#define CUDA_CHECK(call)                                                            \
+  do {                                                                              \
+    cudaError_t fpn_err_ = (call);                                                  \
+    if (fpn_err_ != cudaSuccess)                                                    \
+      FPN_THROW(std::string("CUDA Error: ") + cudaGetErrorString(fpn_err_) +        \
+                "\nCall: " #call);                                                  \
+  } while (0)
+
+enum class FPNDataType {
+  FLOAT32,
+  FLOAT16,
+  BFLOAT16,
+  INT8,
+  INT4,
+  TFLOAT32,
+  FP8_E4M3,
+  FP8_E5M2,
+  DOUBLE,
+  INT16,
+  UINT8,
+  COMPLEX64,
+  BOOL,
+  AUTO
+};
+
+// Memory layout of a 4-D feature map [N, C, H, W].  NCHW is the reference's
+// (torch-contiguous) layout; NHWC is torch.channels_last, the layout the
+// tensor-core path computes in.
+enum class FPNLayout { NCHW = 0, NHWC = 1 };
+
+enum class FPNActivation { NONE, RELU, LEAKY_RELU, SWISH };
+
+struct FPNDimensions {
+  int batch_size;
+  int channels;
+  int height;
+  int width;
+  size_t stride_bytes;
+};
+
+struct FPNLevelConfig {
+  FPNDimensions input_dim;
+  FPNDimensions output_dim;
+  float scale_factor;
+  bool enable_output_conv;
+};
+
+inline size_t fpn_element_size(FPNDataType t) {
+  switch (t) {
+    case FPNDataType::FLOAT32:
+    case FPNDataType::TFLOAT32:
+      return 4;
+    case FPNDataType::FLOAT16:
+    case FPNDataType::BFLOAT16:
+    case FPNDataType::INT16:
+      return 2;
+    case FPNDataType::DOUBLE:
+    case FPNDataType::COMPLEX64:
+      return 8;
+    default:
+      return 1;
+  }
+}
+
+template <typename T>
+struct FPNTensor {
+  T* data;
+  FPNDimensions dims;
+  FPNDataType dtype;
+  bool is_device_memory;
+  FPNLayout layout = FPNLayout::NCHW;
+
+  size_t total_elements() const {
+    return static_cast<size_t>(dims.batch_size) * dims.channels * dims.height * dims.width;
+  }
+  size_t size_bytes() const { return total_elements() * fpn_element_size(dtype); }
+};
+
+struct FPNKernelConfig {
+  int tile_size = 16;            // 3x3 conv spatial tile width (tile height = 128 / width); 0 = auto
+  int channels_per_thread = 8;   // accepted for API compatibility
+  int shared_mem_size = 0;       // accepted for API compatibility
+  bool use_tensor_cores = true;  // false forces the fp32 CUDA-core path
+  bool enable_async_copy = true; // TMA is always used on the tensor-core path
+  FPNActivation activation = FPNActivation::NONE;
+  bool enable_graph_capture = true;  // replay the P5->P2 schedule as one CUDA graph
+};
+
+struct FPNWeights {
+  void* lateral_conv_weights[4];  // packed in the compute dtype, [256][Cin]
+  float* lateral_conv_bias[4];
+  void* output_conv_weights[4];   // packed in the compute dtype, [256][9][256]
+  float* output_conv_bias[4];
+  size_t lateral_weight_sizes[4];
+  size_t output_weight_sizes[4];
+  bool weights_initialized;
+};
+
+struct FPNPerformanceMetrics {
+  float forward_time_ms;
+  float memory_bandwidth_gb_s;
+  float compute_utilization;  // achieved TFLOP/s / measured-peak TFLOP/s of the last timed forward
+  size_t peak_memory_usage_bytes;
+  int num_kernel_launches;  // counted, not estimated
+  // Per-kernel device times of the last profiled forward:
+  // [lat P5, 3x3 P5, lat P4, 3x3 P4, lat P3, 3x3 P3, lat P2, 3x3 P2]
+  float kernel_times_ms[8];
+};

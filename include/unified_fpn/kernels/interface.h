@@ -1,0 +1,88 @@
+// Kernel-level C++ API of the B200 FPN-neck library: one launcher per kernel.
+//
+// Replaces the reference's kernel interface header
+// include/unified_fpn/kernels/interface.h:5-109, which declared the raw
+// __global__ templates (lateral_conv_kernel, bilinear_upsample_kernel,
+// depthwise_conv_kernel, element_wise_add_kernel, ...).  Here the kernels stay
+// private to the library and each is reached through a stream-ordered
+// launcher taking plain device pointers; the tensor-core kernels additionally
+// take a TcPlan built once per (pointers, shapes) so a launch is replayable
+// (and capturable in a CUDA graph).
+//   lateral_conv_kernel (:18-29)              -> plan_tc_lateral / launch_fp32_lateral
+//   bilinear_upsample_kernel (:31-43)
+//     + element_wise_add_kernel (:79-85)      -> launch_upsample_add
+//   depthwise_conv_kernel (:45-56)            -> plan_tc_conv3x3 / launch_fp32_conv3x3
+//   (no counterpart: P6)                      -> launch_p6
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ufpn {
+
+// Values match FPNDataType in include/unified_fpn/core/types.h (FLOAT32 = 0, FLOAT16 = 1,
+// BFLOAT16 = 2, FP8_E4M3 = 6) and the ufpn_dtype codes of the C ABI.
+enum class DType : int { F32 = 0, F16 = 1, BF16 = 2, E4M3 = 6 };
+enum class Layout : int { NCHW = 0, NHWC = 1 };
+
+inline int dtype_size(DType d) {
+  return d == DType::F32 ? 4 : (d == DType::E4M3 ? 1 : 2);
+}
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---- bandwidth kernels (simt_kernels.cu)
+cudaError_t launch_upsample_add(DType dt, const void* coarse, const void* lat, void* out, int N,
+                                int C, int Hc, int Wc, int H, int W, int align_corners,
+                                Layout layout, cudaStream_t s);
+cudaError_t launch_p6(DType dt, const void* in, void* out, int N, int C, int H, int W,
+                      Layout layout, cudaStream_t s);
+cudaError_t launch_transpose(DType dt, const void* in, void* out, int N, int C, int HW,
+                             bool to_nhwc, cudaStream_t s);
+cudaError_t launch_convert_weights(DType dt, const float* in, void* out, long long n,
+                                   cudaStream_t s);
+cudaError_t launch_pack_conv3x3(DType dt, const float* in, void* out, int Cout, int Cin,
+                                cudaStream_t s);
+cudaError_t launch_fp32_lateral(const float* x, const float* w, const float* bias,
+                                const float* coarse, float* out, int N, int Cin, int Cout, int H,
+                                int W, int Hc, int Wc, cudaStream_t s);
+cudaError_t launch_fp32_conv3x3(const float* x, const float* w, const float* bias, float* out,
+                                int N, int Cin, int Cout, int H, int W, cudaStream_t s);
+
+// ---- tensor-core kernels (tc_kernels.cu)
+// Spatial tiling of the 3x3 implicit GEMM: tile_w * tile_h = 128 output pixels.
+struct Conv3x3Tiling {
+  int tile_w = 16;
+  int tile_h = 8;
+};
+
+// Everything one tensor-core launch needs, built on the host once per
+// (pointers, shapes) and replayable: the two TMA descriptors plus the
+// kernel argument block.
+struct TcPlan {
+  alignas(64) CUtensorMap map_a;
+  alignas(64) CUtensorMap map_b;
+  unsigned char args[256];  // TcGemmArgs, opaque outside tc_kernels.cu
+  int mode = 0;             // 0 lateral, 1 conv3x3
+  DType dtype = DType::BF16;
+  int grid = 0;
+  int num_tiles = 0;
+};
+
+// Lateral 1x1 (+ optional fused bilinear upsample-add of the coarser merged map).
+//   x: NHWC [N][H][W][Cin]; w: [256][Cin] (dtype, K-major); bias fp32 [256];
+//   coarse: NHWC [N][Hc][Wc][256] or null; out: NHWC [N][H][W][256].
+cudaError_t plan_tc_lateral(TcPlan& plan, DType dt, const void* x, const void* w,
+                            const float* bias, const void* coarse, void* out, int N, int Cin,
+                            int H, int W, int Hc, int Wc, int* status, int max_ctas);
+// 3x3 pad-1 conv, 256 -> 256: x NHWC [N][H][W][256]; w: [256][9][256]; out NHWC;
+// p6 (optional) NHWC [N][ceil(H/2)][ceil(W/2)][256].
+cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w,
+                            const float* bias, void* out, void* p6, int N, int H, int W,
+                            Conv3x3Tiling tiling, int* status, int max_ctas);
+cudaError_t launch_tc(const TcPlan& plan, cudaStream_t s);
+
+// Number of SMs on the current device (cached).
+int sm_count();
+
+}  // namespace ufpn

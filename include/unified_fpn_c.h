@@ -1,0 +1,203 @@
+/* C ABI of the B200 FPN-neck library (libunified_fpn_b200.so).
+ *
+ * Plain pointers, sizes and status codes; no C++ or torch types.  Every entry
+ * point enqueues work on the given CUDA stream (NULL = legacy default stream)
+ * and returns without blocking the host unless stated otherwise.  On failure
+ * an entry point returns a non-zero UFPN_ERR_* code and ufpn_last_error()
+ * describes it; nothing here calls exit().
+ *
+ * Each declaration names the reference interface it replaces (paths are
+ * relative to the sanowl/-UnifiedFPN source tree).
+ */
+#ifndef UNIFIED_FPN_C_H_
+#define UNIFIED_FPN_C_H_
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define UFPN_OK 0
+#define UFPN_ERR_INVALID_ARG 1
+#define UFPN_ERR_CUDA 2
+#define UFPN_ERR_UNSUPPORTED 3
+#define UFPN_ERR_DEVICE_TIMEOUT 4
+#define UFPN_ERR_STATE 5
+#define UFPN_ERR_ALIGNMENT 6
+
+/* dtype codes: the ordinals of FPNDataType (include/unified_fpn/core/types.h:208-223) */
+#define UFPN_DTYPE_F32 0
+#define UFPN_DTYPE_F16 1
+#define UFPN_DTYPE_BF16 2
+#define UFPN_DTYPE_E4M3 6
+
+#define UFPN_LAYOUT_NCHW 0 /* torch contiguous */
+#define UFPN_LAYOUT_NHWC 1 /* torch channels_last */
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* ufpn_last_error(void);
+/* Library version, major * 10000 + minor * 100 + patch. */
+int ufpn_version(void);
+/* Reads (and with reset != 0 clears) the status word the tensor-core kernels of
+ * the standalone entry points write when a pipeline wait times out on the
+ * current device; 0 = no error.  Synchronises the device. */
+int ufpn_device_status(int reset, int* status_out);
+
+/* ---------------------------------------------------------------- engine
+ * Replaces class UnifiedFPNCore (lib/core/fpn_engine.cu:10-416) and the
+ * PyTorchFPNWrapper state it is driven through (python/fpn_pytorch.cpp:9-137). */
+typedef struct ufpn_core ufpn_core;
+
+/* fpn_engine.cu:29-35 (UnifiedFPNCore(size_t workspace_size)) */
+int ufpn_core_create(int device, size_t workspace_bytes, ufpn_core** out);
+/* fpn_engine.cu:37-41 */
+void ufpn_core_destroy(ufpn_core* core);
+/* fpn_engine.cu:95-106 (configure_levels).  in_channels/heights/widths: C2..C5. */
+int ufpn_core_configure_levels(ufpn_core* core, int batch, const int* in_channels,
+                               const int* heights, const int* widths, int output_channels,
+                               int dtype, int layout);
+/* fpn_engine.cu:108-150 (allocate_weights).  in_channels: Cin of C2..C5. */
+int ufpn_core_allocate_weights(ufpn_core* core, const int* in_channels, int output_channels);
+/* fpn_engine.cu:169-189 (set_weights).  fp32, host or device memory. */
+int ufpn_core_set_weights(ufpn_core* core, int level, const float* lateral_w,
+                          const float* lateral_b, const float* output_w, const float* output_b);
+/* fpn_engine.cu:191-245 (forward).  inputs: C2..C5 device pointers in the configured
+ * dtype/layout; outputs: P2..P5; p6 may be NULL. */
+int ufpn_core_forward(ufpn_core* core, const void* const* inputs, void* const* outputs,
+                      void* p6, void* stream);
+/* fpn_engine.cu:404-406 (set_kernel_config) via fpn_pytorch.cpp:189-209.
+ * tile_size: 3x3 tile width (8..128, 0 = autotuned/heuristic); activation:
+ * FPNActivation ordinal (only NONE is supported). */
+int ufpn_core_set_kernel_config(ufpn_core* core, int tile_size, int channels_per_thread,
+                                int use_tensor_cores, int activation, int enable_graph_capture);
+/* fpn_engine.cu:408-415 (get_memory_usage) */
+size_t ufpn_core_get_memory_usage(const ufpn_core* core);
+/* fpn_pytorch.cpp:171-187 (get_performance_breakdown): kernel_times_ms[8], metrics[5] =
+ * {forward_ms, GB/s, compute utilisation, peak MiB, kernel launches}. */
+int ufpn_core_get_performance_metrics(const ufpn_core* core, float* kernel_times_ms,
+                                      float* metrics);
+/* Time each kernel of the next forward with events (serialised). */
+int ufpn_core_set_profiling(ufpn_core* core, int enable);
+/* lib/utils/auto_tuner.cu:213-275 (auto_tune_lateral_conv), for every level of the neck. */
+int ufpn_core_autotune(ufpn_core* core, const void* const* inputs, void* const* outputs,
+                       void* p6, void* stream, int iterations);
+/* auto_tuner.cu:305-323 (save_tuning_results) plus the missing load. */
+int ufpn_core_save_tuning(const ufpn_core* core, const char* path);
+int ufpn_core_load_tuning(ufpn_core* core, const char* path);
+int ufpn_core_device_status(ufpn_core* core, int reset, int* status_out);
+
+/* ---------------------------------------------------------------- standalone ops */
+
+/* 1x1 lateral conv + bias, optionally fused with the top-down bilinear
+ * upsample-add of the coarser merged map: out = conv1x1(x) + b [+ up(coarse)].
+ * Replaces fpn_lateral_conv (python/fpn_pytorch.cpp:293-326) and
+ * lateral_conv_kernel (lib/kernels/compute/fpn_compute_kernels.cu:127-230).
+ *   dtype F32: layout must be NCHW, w fp32 [Cout][Cin], CUDA-core fp32 path.
+ *   dtype F16/BF16: layout must be NHWC, w in dtype [256][Cin], Cout = 256,
+ *   tcgen05 path.  coarse: same dtype/layout, [N][Cout][Hc][Wc] logical, or NULL. */
+int ufpn_lateral_conv(int dtype, int layout, const void* x, const void* w, const float* bias,
+                      const void* coarse, void* out, int N, int Cin, int H, int W, int Cout,
+                      int Hc, int Wc, void* stream);
+
+/* 3x3 pad-1 output conv 256->256 (+ optional P6 = P5[::2, ::2]).
+ * Replaces launch_output_conv / depthwise_conv_kernel (fpn_engine.cu:315-362,
+ * fpn_compute_kernels.cu:277-340) with the full conv of the standard neck.
+ *   dtype F16/BF16: NHWC x, w in dtype packed [256][9][256] (ufpn_pack_conv3x3_weights).
+ *   dtype F32: NCHW x, w fp32 [256][256][3][3].
+ * tile_w: spatial tile width of the tensor-core path (8..128, 0 = heuristic). */
+int ufpn_conv3x3(int dtype, const void* x, const void* w, const float* bias, void* out,
+                 void* p6, int N, int H, int W, int tile_w, void* stream);
+
+/* out = lateral + bilinear_upsample(coarse -> H x W); lateral may be NULL (pure upsample).
+ * Replaces launch_upsample_and_add (fpn_engine.cu:274-313) = bilinear_upsample_kernel +
+ * element_wise_add_kernel (fpn_compute_kernels.cu:232-275, 397-409). */
+int ufpn_upsample_add(int dtype, int layout, const void* coarse, const void* lateral, void* out,
+                      int N, int C, int Hc, int Wc, int H, int W, int align_corners,
+                      void* stream);
+
+/* P6 = max_pool2d(P5, kernel 1, stride 2).  No reference counterpart (the reference never
+ * produces P6 although it takes C6, python/fpn_pytorch.cpp:84-86). */
+int ufpn_p6_maxpool(int dtype, int layout, const void* p5, void* p6, int N, int C, int H, int W,
+                    void* stream);
+
+/* fp32 [Cout][Cin][3][3] (device) -> dtype [Cout][9][Cin] K-major packing for ufpn_conv3x3. */
+int ufpn_pack_conv3x3_weights(int dtype, const float* w, void* out, int Cout, int Cin,
+                              void* stream);
+/* fp32 (device) -> dtype element conversion (lateral weight packing). */
+int ufpn_convert_weights(int dtype, const float* w, void* out, long long count, void* stream);
+/* NCHW <-> NHWC layout conversion. */
+int ufpn_layout_convert(int dtype, const void* in, void* out, int N, int C, int H, int W,
+                        int to_nhwc, void* stream);
+
+/* ---------------------------------------------------------------- reference C ABI
+ * Same names and argument meaning as the reference's exported functions.  NHWC
+ * tensors (the layout of the reference's kernels).  These time the launch with
+ * events and synchronise, like the originals. */
+
+/* lib/kernels/memory/fast_upsample_kernels.cu:622-647 */
+cudaError_t launch_production_upsample_float(const float* input, float* output, int batch_size,
+                                             int channels, int in_height, int in_width,
+                                             int out_height, int out_width, int align_corners,
+                                             float* kernel_time_ms, float* bandwidth_gb_s);
+/* fast_upsample_kernels.cu:649-674 (half = IEEE fp16, passed as uint16_t storage) */
+cudaError_t launch_production_upsample_half(const void* input, void* output, int batch_size,
+                                            int channels, int in_height, int in_width,
+                                            int out_height, int out_width, int align_corners,
+                                            float* kernel_time_ms, float* bandwidth_gb_s);
+/* lib/kernels/memory/upsample_specializations.cu:492-539 */
+cudaError_t launch_production_upsample_bfloat16(const void* input, void* output,
+                                                int batch_size, int channels, int in_height,
+                                                int in_width, int out_height, int out_width,
+                                                int align_corners, float* kernel_time_ms,
+                                                float* bandwidth_gb_s);
+
+/* lib/kernels/memory/upsample_host_interface.cpp:516-522 */
+void* create_upsample_engine(int device_id);
+/* upsample_host_interface.cpp:527-531 */
+void destroy_upsample_engine(void* engine);
+/* upsample_host_interface.cpp:536-585; metrics_out[4] = {ms, GB/s, util, bytes} */
+int production_upsample_float(void* engine, const float* input, float* output, int batch_size,
+                              int channels, int in_height, int in_width, int out_height,
+                              int out_width, float scale_y, float scale_x, int align_corners,
+                              float* metrics_out);
+/* upsample_host_interface.cpp:590-594 */
+void print_upsample_profiling_summary(void* engine);
+/* upsample_host_interface.cpp:599-609 (CSV) */
+int export_upsample_profiling_data(void* engine, const char* filename);
+
+/* lib/utils/auto_tuner.cu:8-25: the reference's TuningResult carries a std::string;
+ * this C-layout version carries a fixed buffer instead. */
+typedef struct {
+  int tile_w;              /* chosen 3x3 tile width (lateral: 0) */
+  int tile_h;
+  int num_ctas;            /* persistent CTAs launched */
+  float time_ms;           /* measured */
+  float performance_gflops;
+  float memory_bandwidth_gb_s;
+  char architecture_name[32];
+} TuningResult;
+
+/* auto_tuner.cu:328-333: times the tensor-core lateral (bf16) on a synthetic problem of
+ * this shape for every CTA-count candidate; out_channels must be 256.  Returns a pointer
+ * to a per-shape cached result (valid until process exit), NULL on error. */
+TuningResult* fpn_auto_tune_lateral_conv(int batch_size, int in_channels, int out_channels,
+                                         int height, int width);
+/* auto_tuner.cu:335-338 */
+void fpn_auto_tune_save_results(const char* filename);
+
+#ifdef __cplusplus
+}
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#endif /* UNIFIED_FPN_C_H_ */

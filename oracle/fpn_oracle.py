@@ -1,0 +1,197 @@
+"""CPU oracle for the FPN neck -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline / reference arm
+may import this module, and only as the checker (or as the timed CPU baseline).
+The library never routes through it.
+
+What it restates (paths relative to the sanowl/-UnifiedFPN source tree):
+
+* ``bilinear_upsample_nchw`` -- the reference's host reference implementation
+  ``cpu_bilinear_upsample_reference`` (benchmarks/upsample_benchmark.cu:24-108):
+  scale = in/out (or (in-1)/(out-1) with align_corners), source coordinate
+  (o + 0.5) * scale - 0.5 clamped to [0, in-1], y1 = min(y0 + 1, in - 1),
+  corner weights (1-wy)(1-wx), (1-wy)wx, wy(1-wx), wy*wx.  Vectorised numpy,
+  fp32 arithmetic in the same order.  Pinned against the reference's own
+  compiled function (oracle/_ref, built by oracle/Makefile) through the golden
+  vectors in tests/golden/.
+* ``lateral_conv`` -- lateral_conv_kernel (lib/kernels/compute/fpn_compute_kernels.cu:127-230):
+  out[o, p] = sum_c in[c, p] * W[o, c] + bias[o].
+* ``fpn_neck`` -- the top-down schedule of UnifiedFPNCore::forward
+  (lib/core/fpn_engine.cu:191-245) with the standard-neck semantics the library
+  implements: M5 = lat(C5); M_l = lat(C_l) + up(M_{l+1}); P_l = conv3x3(M_l)
+  (full 256->256, pad 1, bias); P6 = max_pool2d(P5, 1, 2).  The 3x3 conv and
+  max-pool use torch's CPU kernels (the reference has no CPU version of them;
+  its device kernel is a depthwise 3x3, fpn_compute_kernels.cu:277-340).
+
+Tolerances (fp32 <= 1e-4, bf16/fp16 <= 1e-2, FP8 <= 3e-2) are relative to the
+largest magnitude of the reference output: ``rel_err(y, ref) = max|y - ref| / max|ref|``.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+TOL = {"f32": 1e-4, "f16": 1e-2, "bf16": 1e-2, "e4m3": 3e-2}
+
+
+# ----------------------------------------------------------------------------- bilinear
+def _src_index(out_size: int, in_size: int, align_corners: bool) -> tuple[np.ndarray, ...]:
+    """Per output index: (i0, i1, w) following upsample_benchmark.cu:37-69."""
+    o = np.arange(out_size, dtype=np.float32)
+    if align_corners:
+        scale = np.float32((in_size - 1) / (out_size - 1)) if out_size > 1 else np.float32(0)
+        src = o * scale if out_size > 1 else np.zeros_like(o)
+    else:
+        scale = np.float32(np.float32(in_size) / np.float32(out_size))
+        src = (o + np.float32(0.5)) * scale - np.float32(0.5)
+    src = np.maximum(np.float32(0), np.minimum(src, np.float32(in_size - 1))).astype(np.float32)
+    i0 = np.floor(src).astype(np.int64)
+    i1 = np.minimum(i0 + 1, in_size - 1)
+    w = (src - i0.astype(np.float32)).astype(np.float32)
+    return i0, i1, w
+
+
+def bilinear_upsample_nchw(x: np.ndarray, out_h: int, out_w: int, align_corners: bool = False) -> np.ndarray:
+    """fp32 NCHW bilinear resize, restating upsample_benchmark.cu:24-108."""
+    x = np.asarray(x, dtype=np.float32)
+    _, _, H, W = x.shape
+    y0, y1, wy = _src_index(out_h, H, align_corners)
+    x0, x1, wx = _src_index(out_w, W, align_corners)
+    wy = wy[:, None]
+    wx = wx[None, :]
+    v00 = x[:, :, y0][:, :, :, x0]
+    v01 = x[:, :, y0][:, :, :, x1]
+    v10 = x[:, :, y1][:, :, :, x0]
+    v11 = x[:, :, y1][:, :, :, x1]
+    one = np.float32(1)
+    # same association as the reference: v00*(1-wy)*(1-wx) + v01*(1-wy)*wx + ...
+    return (v00 * (one - wy) * (one - wx) + v01 * (one - wy) * wx + v10 * wy * (one - wx)
+            + v11 * wy * wx).astype(np.float32)
+
+
+def bilinear_upsample_t(x: torch.Tensor, size) -> torch.Tensor:
+    """torch-CPU bilinear (align_corners=False), used inside the neck oracle."""
+    return F.interpolate(x, size=size, mode="bilinear", align_corners=False)
+
+
+# ----------------------------------------------------------------------------- neck
+def lateral_conv(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """out[n, o, y, x] = sum_c x[n, c, y, x] * w[o, c] + b[o] (fpn_compute_kernels.cu:127-230)."""
+    return F.conv2d(x, w.reshape(w.shape[0], -1, 1, 1), b)
+
+
+def conv3x3(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    return F.conv2d(x, w, b, padding=1)
+
+
+def p6_maxpool(p5: torch.Tensor) -> torch.Tensor:
+    return F.max_pool2d(p5, kernel_size=1, stride=2)
+
+
+@dataclass
+class NeckWeights:
+    lat_w: list  # [256, Cin] fp32
+    lat_b: list  # [256]
+    out_w: list  # [256, 256, 3, 3]
+    out_b: list  # [256]
+
+
+def fpn_neck(feats, wts: NeckWeights, return_merged: bool = False):
+    """fp32 CPU neck.  feats: C2..C5 (NCHW float tensors).  Returns [P2, P3, P4, P5, P6]."""
+    feats = [f.float() for f in feats]
+    merged = [None] * 4
+    for l in (3, 2, 1, 0):
+        m = lateral_conv(feats[l], wts.lat_w[l].float(), wts.lat_b[l].float())
+        if l < 3:
+            m = m + bilinear_upsample_t(merged[l + 1], m.shape[-2:])
+        merged[l] = m
+    outs = [conv3x3(merged[l], wts.out_w[l].float(), wts.out_b[l].float()) for l in range(4)]
+    outs.append(p6_maxpool(outs[3]))
+    return (outs, merged) if return_merged else outs
+
+
+def fused_lateral_upsample(c3: torch.Tensor, p4: torch.Tensor, w: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """Single-level op: conv1x1(C3) + bilinear_upsample(P4, C3's size)."""
+    return lateral_conv(c3.float(), w.float(), b.float()) + bilinear_upsample_t(p4.float(), c3.shape[-2:])
+
+
+# ----------------------------------------------------------------------------- synthetic inputs
+R50_CHANNELS = (256, 512, 1024, 2048)
+SWIN_CHANNELS = (128, 256, 512, 1024)
+
+
+def level_sizes(h: int, w: int):
+    """Spatial sizes of C2..C5 for an image: strides 4, 8, 16, 32 (ceil division)."""
+    return [(math.ceil(h / s), math.ceil(w / s)) for s in (4, 8, 16, 32)]
+
+
+def make_features(batch, channels, sizes, seed=0, dist="relu_normal"):
+    """C2..C5 as fp32 NCHW CPU tensors (generation order C2 -> C5)."""
+    g = torch.Generator().manual_seed(seed)
+    out = []
+    for c, (h, w) in zip(channels, sizes):
+        x = torch.randn(batch, c, h, w, generator=g)
+        if dist == "relu_normal":
+            x = x.clamp_min(0)
+        out.append(x)
+    return out
+
+
+def make_weights(channels, seed=1, bias_scale=0.0) -> NeckWeights:
+    """Kaiming-normal (fan_in) weights, per level lateral then 3x3; biases U(-s, s) or zero."""
+    g = torch.Generator().manual_seed(seed)
+    lw, lb, ow, ob = [], [], [], []
+    for c in channels:
+        lw.append(torch.randn(256, c, generator=g) * math.sqrt(2.0 / c))
+        lb.append((torch.rand(256, generator=g) * 2 - 1) * bias_scale)
+        ow.append(torch.randn(256, 256, 3, 3, generator=g) * math.sqrt(2.0 / (256 * 9)))
+        ob.append((torch.rand(256, generator=g) * 2 - 1) * bias_scale)
+    return NeckWeights(lw, lb, ow, ob)
+
+
+def config1_inputs(seed=0):
+    """fp32 NCHW b1: C3 [1,512,64,64] ~N(0,1), P4 [1,256,32,32] ~N(0,1); W [256,512]
+    Kaiming-normal (fan_in); bias U(-0.1, 0.1)."""
+    g = torch.Generator().manual_seed(seed)
+    c3 = torch.randn(1, 512, 64, 64, generator=g)
+    p4 = torch.randn(1, 256, 32, 32, generator=g)
+    w = torch.randn(256, 512, generator=g) * math.sqrt(2.0 / 512)
+    b = (torch.rand(256, generator=g) * 2 - 1) * 0.1
+    return c3, p4, w, b
+
+
+# ----------------------------------------------------------------------------- FP8 (e4m3)
+E4M3_MAX = 448.0
+
+
+def quantize_e4m3(x: torch.Tensor, per_channel_dim: int | None = None):
+    """Symmetric e4m3 quantisation with scale = absmax / 448 (per tensor, or per
+    slice along ``per_channel_dim``).  Returns (dequantised fp32 tensor, scale)."""
+    x = x.float()
+    if per_channel_dim is None:
+        amax = x.abs().max().clamp_min(1e-12)
+        scale = amax / E4M3_MAX
+        q = (x / scale).to(torch.float8_e4m3fn)
+        return q.float() * scale, scale
+    dims = [d for d in range(x.dim()) if d != per_channel_dim]
+    amax = x.abs().amax(dim=dims, keepdim=True).clamp_min(1e-12)
+    scale = amax / E4M3_MAX
+    q = (x / scale).to(torch.float8_e4m3fn)
+    return q.float() * scale, scale
+
+
+# ----------------------------------------------------------------------------- checking
+def rel_err(y, ref) -> float:
+    y = torch.as_tensor(y).float()
+    ref = torch.as_tensor(ref).float()
+    denom = ref.abs().max().item()
+    return (y - ref).abs().max().item() / (denom if denom > 0 else 1.0)
+
+
+def round_to(x: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """Rounds fp32 values to ``dtype`` and back (the oracle's inputs for 16-bit runs)."""
+    return x.to(dtype).float()

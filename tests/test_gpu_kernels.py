@@ -1,0 +1,211 @@
+"""GPU parity tests of the standalone kernels, called through the C ABI
+(libunified_fpn_b200.so via ctypes), against the CPU oracle."""
+import ctypes
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import fpn_oracle as O
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+BF16_TOL = O.TOL["bf16"]   # 1e-2 relative to max |ref|
+F32_TOL = O.TOL["f32"]     # 1e-4
+
+
+def _golden_bilinear():
+    z = np.load(GOLDEN / "bilinear_ref.npz")
+    n = len([k for k in z.files if k.endswith("_shape")])
+    return [(z[f"case{i}_shape"], z[f"case{i}_in"], z[f"case{i}_out"]) for i in range(n)]
+
+
+def _cl(x):
+    return x.contiguous(memory_format=torch.channels_last)
+
+
+# ----------------------------------------------------------------------------- upsample
+@pytest.mark.parametrize("case", range(9))
+def test_reference_abi_upsample_float_matches_reference_golden(cuda_device, case):
+    """launch_production_upsample_float (NHWC, reference C ABI) vs the reference's own
+    host implementation's outputs."""
+    from unified_fpn import _lib
+    shape, x, ref = _golden_bilinear()[case]
+    n, c, ih, iw, oh, ow, ac = [int(v) for v in shape]
+    xd = _cl(torch.from_numpy(x).to(cuda_device))
+    out = _cl(torch.empty(n, c, oh, ow, device=cuda_device))
+    ms, gbs = ctypes.c_float(), ctypes.c_float()
+    rc = _lib.lib.launch_production_upsample_float(xd.data_ptr(), out.data_ptr(), n, c, ih, iw, oh, ow, ac,
+                                                   ctypes.byref(ms), ctypes.byref(gbs))
+    assert rc == 0
+    np.testing.assert_allclose(out.cpu().numpy(), ref, rtol=0, atol=2e-6)
+
+
+@pytest.mark.parametrize("case", range(9))
+def test_upsample_nchw_fp32_matches_reference_golden(cuda_device, case):
+    import unified_fpn as U
+    shape, x, ref = _golden_bilinear()[case]
+    n, c, ih, iw, oh, ow, ac = [int(v) for v in shape]
+    y = U.fpn_upsample_add(torch.from_numpy(x).to(cuda_device), None, size=(oh, ow), align_corners=bool(ac))
+    np.testing.assert_allclose(y.cpu().numpy(), ref, rtol=0, atol=2e-6)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("layout", ["nhwc", "nchw"])
+@pytest.mark.parametrize("sizes", [((2, 256, 25, 38), (50, 76)), ((1, 256, 84, 50), (167, 100)),
+                                   ((1, 40, 7, 9), (13, 18))])
+def test_upsample_add(cuda_device, dtype, layout, sizes):
+    import unified_fpn as U
+    (n, c, hc, wc), (h, w) = sizes
+    g = torch.Generator().manual_seed(5)
+    coarse = torch.randn(n, c, hc, wc, generator=g).to(dtype)
+    lat = torch.randn(n, c, h, w, generator=g).to(dtype)
+    cd, ld = coarse.to(cuda_device), lat.to(cuda_device)
+    if layout == "nhwc":
+        cd, ld = _cl(cd), _cl(ld)
+    y = U.fpn_upsample_add(cd, ld)
+    ref = lat.float() + O.bilinear_upsample_t(coarse.float(), (h, w))
+    tol = F32_TOL if dtype == torch.float32 else BF16_TOL
+    assert O.rel_err(y.cpu(), ref) < tol
+    if layout == "nhwc":
+        assert y.is_contiguous(memory_format=torch.channels_last)
+
+
+def test_reference_abi_upsample_half_and_bf16(cuda_device):
+    from unified_fpn import _lib
+    x = torch.randn(2, 64, 13, 19)
+    ref = O.bilinear_upsample_t(x, (25, 38))
+    for dt, fn in ((torch.float16, _lib.lib.launch_production_upsample_half),
+                   (torch.bfloat16, _lib.lib.launch_production_upsample_bfloat16)):
+        xd = _cl(x.to(dt).to(cuda_device))
+        out = _cl(torch.empty(2, 64, 25, 38, dtype=dt, device=cuda_device))
+        assert fn(xd.data_ptr(), out.data_ptr(), 2, 64, 13, 19, 25, 38, 0, None, None) == 0
+        assert O.rel_err(out.cpu(), O.bilinear_upsample_t(x.to(dt).float(), (25, 38))) < BF16_TOL
+
+
+def test_upsample_engine_abi(cuda_device, tmp_path):
+    from unified_fpn import _lib
+    lib = _lib.lib
+    eng = lib.create_upsample_engine(0)
+    assert eng
+    x = _cl(torch.randn(1, 32, 8, 8, device=cuda_device))
+    out = _cl(torch.empty(1, 32, 16, 16, device=cuda_device))
+    m = (ctypes.c_float * 4)()
+    assert lib.production_upsample_float(eng, x.data_ptr(), out.data_ptr(), 1, 32, 8, 8, 16, 16, 0.5, 0.5, 0, m) == 0
+    assert m[3] > 0
+    csv = tmp_path / "prof.csv"
+    assert lib.export_upsample_profiling_data(eng, str(csv).encode()) == 0
+    assert "bilinear_upsample_f32" in csv.read_text()
+    lib.destroy_upsample_engine(eng)
+    ref = O.bilinear_upsample_t(x.cpu().contiguous(), (16, 16))
+    assert O.rel_err(out.cpu(), ref) < F32_TOL
+
+
+# ----------------------------------------------------------------------------- P6
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("layout", ["nhwc", "nchw"])
+def test_p6_exact(cuda_device, dtype, layout):
+    import unified_fpn as U
+    p5 = torch.randn(2, 256, 25, 38).to(dtype).to(cuda_device)
+    if layout == "nhwc":
+        p5 = _cl(p5)
+    p6 = U.fpn_p6(p5)
+    assert p6.shape == (2, 256, 13, 19)
+    assert torch.equal(p6.cpu(), O.p6_maxpool(p5.cpu().float()).to(dtype))
+
+
+# ----------------------------------------------------------------------------- lateral (tcgen05)
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", [(1, 64, 7, 9), (2, 256, 20, 30), (1, 96, 16, 16), (2, 2048, 5, 7),
+                                   (1, 512, 33, 40)])
+def test_lateral_tc(cuda_device, dtype, shape):
+    import unified_fpn as U
+    n, cin, h, w = shape
+    g = torch.Generator().manual_seed(cin + h)
+    x = torch.randn(n, cin, h, w, generator=g).to(dtype)
+    wt = (torch.randn(256, cin, generator=g) * (2.0 / cin) ** 0.5)
+    b = torch.rand(256, generator=g) * 0.2 - 0.1
+    y = U.fpn_lateral_conv(_cl(x.to(cuda_device)), wt.to(cuda_device), b.to(cuda_device))
+    torch.cuda.synchronize()
+    assert U.device_status() == 0
+    ref = O.lateral_conv(x.float(), wt.to(dtype).float(), b)
+    assert O.rel_err(y.cpu(), ref) < BF16_TOL
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("geom", [((2, 256, 20, 30), (10, 15)), ((1, 512, 25, 42), (13, 21)),
+                                  ((1, 128, 100, 167), (50, 84)), ((2, 64, 9, 5), (9, 5))])
+def test_lateral_tc_fused_upsample_add(cuda_device, dtype, geom):
+    import unified_fpn as U
+    (n, cin, h, w), (hc, wc) = geom
+    g = torch.Generator().manual_seed(hc * 7 + wc)
+    x = torch.randn(n, cin, h, w, generator=g).to(dtype)
+    coarse = torch.randn(n, 256, hc, wc, generator=g).to(dtype)
+    wt = torch.randn(256, cin, generator=g) * (2.0 / cin) ** 0.5
+    b = torch.rand(256, generator=g) * 0.2 - 0.1
+    y = U.fpn_lateral_conv(_cl(x.to(cuda_device)), wt.to(cuda_device), b.to(cuda_device),
+                           coarse=_cl(coarse.to(cuda_device)))
+    ref = O.lateral_conv(x.float(), wt.to(dtype).float(), b) + O.bilinear_upsample_t(coarse.float(), (h, w))
+    assert O.rel_err(y.cpu(), ref) < BF16_TOL
+    assert U.device_status() == 0
+
+
+def test_lateral_fp32_config1(cuda_device):
+    """Single-level fused op, fp32 NCHW b1: conv1x1(C3 [1,512,64,64]) + up2x(P4 [1,256,32,32])."""
+    import unified_fpn as U
+    c3, p4, w, b = O.config1_inputs(seed=0)
+    y = U.fpn_lateral_conv(c3.to(cuda_device), w.to(cuda_device), b.to(cuda_device), coarse=p4.to(cuda_device))
+    ref = O.fused_lateral_upsample(c3, p4, w, b)
+    assert O.rel_err(y.cpu(), ref) < F32_TOL
+
+
+# ----------------------------------------------------------------------------- 3x3 (tcgen05)
+@pytest.mark.parametrize("tile_w", [8, 16, 32, 64, 128])
+def test_conv3x3_tc_tilings(cuda_device, tile_w):
+    import unified_fpn as U
+    g = torch.Generator().manual_seed(tile_w)
+    x = torch.randn(1, 256, 9, 13, generator=g).to(torch.bfloat16)
+    w = torch.randn(256, 256, 3, 3, generator=g) * (2.0 / 2304) ** 0.5
+    b = torch.rand(256, generator=g) * 0.2 - 0.1
+    y = U.fpn_conv3x3(_cl(x.to(cuda_device)), w.to(cuda_device), b.to(cuda_device), tile_w=tile_w)
+    ref = O.conv3x3(x.float(), w.to(torch.bfloat16).float(), b)
+    assert O.rel_err(y.cpu(), ref) < BF16_TOL
+    assert U.device_status() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", [(2, 25, 38), (1, 50, 84), (1, 1, 1), (3, 17, 5)])
+def test_conv3x3_tc_with_p6(cuda_device, dtype, shape):
+    import unified_fpn as U
+    n, h, w_ = shape
+    g = torch.Generator().manual_seed(h * 100 + w_)
+    x = torch.randn(n, 256, h, w_, generator=g).to(dtype)
+    w = torch.randn(256, 256, 3, 3, generator=g) * (2.0 / 2304) ** 0.5
+    b = torch.rand(256, generator=g) * 0.2 - 0.1
+    y, p6 = U.fpn_conv3x3(_cl(x.to(cuda_device)), w.to(cuda_device), b.to(cuda_device), p6=True)
+    ref = O.conv3x3(x.float(), w.to(dtype).float(), b)
+    assert O.rel_err(y.cpu(), ref) < BF16_TOL
+    assert torch.equal(p6.cpu(), y.cpu()[:, :, ::2, ::2])
+
+
+def test_conv3x3_fp32(cuda_device):
+    import unified_fpn as U
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(1, 256, 11, 14, generator=g)
+    w = torch.randn(256, 256, 3, 3, generator=g) * (2.0 / 2304) ** 0.5
+    b = torch.rand(256, generator=g) * 0.2 - 0.1
+    y = U.fpn_conv3x3(x.to(cuda_device), w.to(cuda_device), b.to(cuda_device))
+    assert O.rel_err(y.cpu(), O.conv3x3(x, w, b)) < F32_TOL
+
+
+def test_layout_convert_roundtrip(cuda_device):
+    from unified_fpn import _lib
+    x = torch.randn(2, 40, 7, 9, device=cuda_device, dtype=torch.bfloat16)
+    y = torch.empty(2, 7, 9, 40, device=cuda_device, dtype=torch.bfloat16)
+    z = torch.empty_like(x)
+    s = torch.cuda.current_stream().cuda_stream
+    assert _lib.lib.ufpn_layout_convert(2, x.data_ptr(), y.data_ptr(), 2, 40, 7, 9, 1, s) == 0
+    assert _lib.lib.ufpn_layout_convert(2, y.data_ptr(), z.data_ptr(), 2, 40, 7, 9, 0, s) == 0
+    assert torch.equal(y, x.permute(0, 2, 3, 1))
+    assert torch.equal(z, x)

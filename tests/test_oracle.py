@@ -1,0 +1,144 @@
+"""CPU tests: the oracle against the reference's golden vectors and against an
+independent numpy restatement of the neck."""
+import ctypes
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import fpn_oracle as O
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _cases():
+    z = np.load(GOLDEN / "bilinear_ref.npz")
+    n = len([k for k in z.files if k.endswith("_shape")])
+    return [(z[f"case{i}_shape"], z[f"case{i}_in"], z[f"case{i}_out"]) for i in range(n)]
+
+
+@pytest.mark.parametrize("case", range(9))
+def test_numpy_bilinear_matches_reference_golden(case):
+    shape, x, ref = _cases()[case]
+    n, c, ih, iw, oh, ow, ac = [int(v) for v in shape]
+    y = O.bilinear_upsample_nchw(x, oh, ow, bool(ac))
+    assert y.shape == ref.shape
+    np.testing.assert_allclose(y, ref, rtol=0, atol=2e-7)
+
+
+def _oracle_c():
+    p = ROOT / "oracle" / "_build" / "libbilinear_oracle.so"
+    if not p.exists():
+        import subprocess
+        subprocess.run(["make", "-C", str(ROOT / "oracle"), str(p)], check=True, capture_output=True)
+    lib = ctypes.CDLL(str(p))
+    lib.oracle_bilinear_upsample_f32.restype = None
+    lib.oracle_bilinear_upsample_f32.argtypes = [ctypes.c_void_p, ctypes.c_void_p] + [ctypes.c_int] * 7
+    return lib
+
+
+@pytest.mark.parametrize("case", range(9))
+def test_c_bilinear_matches_reference_golden(case):
+    lib = _oracle_c()
+    shape, x, ref = _cases()[case]
+    n, c, ih, iw, oh, ow, ac = [int(v) for v in shape]
+    out = np.zeros((n, c, oh, ow), np.float32)
+    lib.oracle_bilinear_upsample_f32(x.ctypes.data, out.ctypes.data, n, c, ih, iw, oh, ow, ac)
+    np.testing.assert_array_equal(out, ref)
+
+
+def test_reference_build_matches_golden_when_present():
+    p = ROOT / "oracle" / "_ref" / "libref_bilinear.so"
+    if not p.exists():
+        pytest.skip("oracle/_ref not built")
+    lib = ctypes.CDLL(str(p))
+    lib.ref_cpu_bilinear_upsample_f32.restype = None
+    lib.ref_cpu_bilinear_upsample_f32.argtypes = [ctypes.c_void_p, ctypes.c_void_p] + [ctypes.c_int] * 7
+    for shape, x, ref in _cases():
+        n, c, ih, iw, oh, ow, ac = [int(v) for v in shape]
+        out = np.zeros((n, c, oh, ow), np.float32)
+        lib.ref_cpu_bilinear_upsample_f32(x.ctypes.data, out.ctypes.data, n, c, ih, iw, oh, ow, ac)
+        np.testing.assert_array_equal(out, ref)
+
+
+def test_torch_interpolate_agrees_with_reference_semantics():
+    for shape, x, ref in _cases():
+        n, c, ih, iw, oh, ow, ac = [int(v) for v in shape]
+        if oh < ih or ow < iw:
+            continue  # torch's downsampling path (antialias off) uses the same formula, but skip
+        y = torch.nn.functional.interpolate(torch.from_numpy(x), size=(oh, ow), mode="bilinear",
+                                            align_corners=bool(ac)).numpy()
+        np.testing.assert_allclose(y, ref, rtol=0, atol=2e-5)
+
+
+def _numpy_neck(feats, wts):
+    """Independent numpy restatement: einsum 1x1, numpy bilinear, explicit 9-tap 3x3."""
+    f = [x.numpy().astype(np.float64) for x in feats]
+    merged = [None] * 4
+    for l in (3, 2, 1, 0):
+        m = np.einsum("nchw,oc->nohw", f[l], wts.lat_w[l].numpy().astype(np.float64))
+        m += wts.lat_b[l].numpy()[None, :, None, None]
+        if l < 3:
+            m += O.bilinear_upsample_nchw(merged[l + 1].astype(np.float32), m.shape[2], m.shape[3])
+        merged[l] = m
+    outs = []
+    for l in range(4):
+        x = np.pad(merged[l], ((0, 0), (0, 0), (1, 1), (1, 1)))
+        H, W = merged[l].shape[2:]
+        w = wts.out_w[l].numpy().astype(np.float64)
+        o = np.zeros((x.shape[0], 256, H, W))
+        for ky in range(3):
+            for kx in range(3):
+                o += np.einsum("nchw,oc->nohw", x[:, :, ky:ky + H, kx:kx + W], w[:, :, ky, kx])
+        outs.append(o + wts.out_b[l].numpy()[None, :, None, None])
+    outs.append(outs[3][:, :, ::2, ::2])
+    return outs
+
+
+def test_torch_neck_matches_numpy_restatement():
+    chans = (16, 24, 32, 40)
+    sizes = [(12, 18), (6, 9), (3, 5), (2, 3)]
+    feats = O.make_features(2, chans, sizes, seed=11, dist="normal")
+    wts = O.make_weights(chans, seed=12, bias_scale=0.1)
+    outs = O.fpn_neck(feats, wts)
+    ref = _numpy_neck(feats, wts)
+    for a, b in zip(outs, ref):
+        assert a.shape == b.shape
+        assert O.rel_err(a, torch.from_numpy(b)) < 1e-5
+
+
+def test_neck_oracle_matches_golden_digest():
+    z = np.load(GOLDEN / "neck_small.npz")
+    chans = tuple(int(c) for c in z["chans"])
+    sizes = [tuple(int(v) for v in s) for s in z["sizes"]]
+    feats = O.make_features(1, chans, sizes, seed=7, dist="normal")
+    wts = O.make_weights(chans, seed=8, bias_scale=0.1)
+    outs = O.fpn_neck(feats, wts)
+    for k, o in enumerate(outs):
+        a = o.numpy().astype(np.float64)
+        assert tuple(a.shape) == tuple(z[f"P{k + 2}_shape"])
+        np.testing.assert_allclose(a.reshape(-1)[z[f"P{k + 2}_idx"]], z[f"P{k + 2}_val"], rtol=1e-5, atol=1e-5)
+        np.testing.assert_allclose(a.sum(), z[f"P{k + 2}_sum"], rtol=1e-4, atol=1e-3)
+        np.testing.assert_allclose((a * a).sum(), z[f"P{k + 2}_sumsq"], rtol=1e-5)
+
+
+def test_p6_is_stride2_subsample():
+    p5 = torch.randn(2, 3, 25, 38)
+    p6 = O.p6_maxpool(p5)
+    assert p6.shape == (2, 3, 13, 19)
+    assert torch.equal(p6, p5[:, :, ::2, ::2])
+
+
+def test_fp8_quantiser_roundtrip_error_bounded():
+    x = torch.randn(64, 300)
+    dq, s = O.quantize_e4m3(x)
+    assert O.rel_err(dq, x) < 0.07
+    dq2, s2 = O.quantize_e4m3(x, per_channel_dim=0)
+    assert s2.shape == (64, 1)
+    assert O.rel_err(dq2, x) < 0.07
+
+
+def test_level_sizes_r50_800x1216():
+    assert O.level_sizes(800, 1216) == [(200, 304), (100, 152), (50, 76), (25, 38)]
