@@ -268,7 +268,8 @@ int ufpn_lateral_conv(int dtype, int layout, const void* x, const void* w, const
   int* status = device_status_word();
   ufpn::TcPlan plan;
   cudaError_t e = ufpn::plan_tc_lateral(plan, dt, x, w, bias, coarse, out, N, Cin, H, W,
-                                        coarse ? Hc : 0, coarse ? Wc : 0, status, 0);
+                                        coarse ? Hc : 0, coarse ? Wc : 0,
+                                        ufpn::default_tiling(H, W), status, 0);
   if (e != cudaSuccess) return cuda_fail(e, "plan lateral");
   e = ufpn::launch_tc(plan, s);
   return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "lateral launch");
@@ -299,16 +300,7 @@ int ufpn_conv3x3(int dtype, const void* x, const void* w, const float* bias, voi
     t.tile_w = tile_w;
     t.tile_h = 128 / tile_w;
   } else {
-    long long best = -1;
-    for (int tw : {16, 8, 32, 64, 128}) {
-      const int th = 128 / tw;
-      const long long a = static_cast<long long>((W + tw - 1) / tw) * tw * ((H + th - 1) / th) * th;
-      if (best < 0 || a < best) {
-        best = a;
-        t.tile_w = tw;
-        t.tile_h = th;
-      }
-    }
+    t = ufpn::default_tiling(H, W);
   }
   int* status = device_status_word();
   ufpn::TcPlan plan;
@@ -547,7 +539,8 @@ TuningResult* fpn_auto_tune_lateral_conv(int batch_size, int in_channels, int ou
     for (int ctas : {sms, sms / 2, 2 * sms / 3}) {
       ufpn::TcPlan plan;
       if (ufpn::plan_tc_lateral(plan, DType::BF16, x, w, b, nullptr, o, batch_size, in_channels,
-                                height, width, 0, 0, device_status_word(), ctas) != cudaSuccess)
+                                height, width, 0, 0, ufpn::default_tiling(height, width),
+                                device_status_word(), ctas) != cudaSuccess)
         continue;
       ufpn::launch_tc(plan, 0);
       cudaEventRecord(e0, 0);

@@ -62,21 +62,7 @@ DType to_dtype(FPNDataType t) {
 
 // Heuristic 3x3 tiling: the tile_w in {8..128} that wastes the fewest padded
 // pixels (ties go to 16, then to the wider tile).
-Conv3x3Tiling heuristic_tiling(int H, int W) {
-  Conv3x3Tiling best;
-  long long best_area = -1;
-  for (int tw : {16, 8, 32, 64, 128}) {
-    const int th = 128 / tw;
-    const long long area = static_cast<long long>((W + tw - 1) / tw) * tw *
-                           static_cast<long long>((H + th - 1) / th) * th;
-    if (best_area < 0 || area < best_area) {
-      best_area = area;
-      best.tile_w = tw;
-      best.tile_h = th;
-    }
-  }
-  return best;
-}
+Conv3x3Tiling heuristic_tiling(int H, int W) { return ufpn::default_tiling(H, W); }
 
 }  // namespace
 
@@ -285,7 +271,8 @@ struct UnifiedFPNCore::Impl {
       TcPlan lat;
       check(ufpn::plan_tc_lateral(lat, dtype, x[l], lat_wp[l], lat_b[l],
                                   l < 3 ? merged[l + 1] : nullptr, merged[l], batch, cin[l], H[l],
-                                  W[l], l < 3 ? H[l + 1] : 0, l < 3 ? W[l + 1] : 0, d_status, 0),
+                                  W[l], l < 3 ? H[l + 1] : 0, l < 3 ? W[l + 1] : 0,
+                                  ufpn::default_tiling(H[l], W[l]), d_status, 0),
             "plan lateral");
       ok(ufpn::launch_tc(lat, main), "lateral launch");
       if (prof_events) cudaEventRecord(prof[1 + 2 * (3 - l)], main);

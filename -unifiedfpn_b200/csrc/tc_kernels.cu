@@ -2,6 +2,7 @@
 // planning and launch.  The device code lives in tc_gemm.cuh.
 #include <cudaTypedefs.h>
 
+#include <cmath>
 #include <cstring>
 #include <mutex>
 
@@ -50,6 +51,7 @@ cudaError_t encode(CUtensorMap* map, DType dt, int rank, const void* base, const
   cuuint64_t d[5], st[4];
   cuuint32_t b[5], es[5];
   for (int i = 0; i < rank; ++i) {
+    if (box[i] < 1 || box[i] > 256) return cudaErrorInvalidValue;
     d[i] = dims[i];
     b[i] = box[i];
     es[i] = 1;
@@ -61,6 +63,42 @@ cudaError_t encode(CUtensorMap* map, DType dt, int rank, const void* base, const
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+// NHWC activation map [N][H][W][C] with a (64, bw, bh, 1) box.
+cudaError_t encode_nhwc(CUtensorMap* map, DType dt, const void* base, int N, int H, int W, int C,
+                        int bw, int bh) {
+  const uint64_t esz = 2;
+  uint64_t dims[4] = {static_cast<uint64_t>(C), static_cast<uint64_t>(W),
+                      static_cast<uint64_t>(H), static_cast<uint64_t>(N)};
+  uint64_t strides[3] = {static_cast<uint64_t>(C) * esz, static_cast<uint64_t>(W) * C * esz,
+                         static_cast<uint64_t>(H) * W * C * esz};
+  uint32_t box[4] = {static_cast<uint32_t>(kTcBlockK), static_cast<uint32_t>(bw),
+                     static_cast<uint32_t>(bh), 1};
+  return encode(map, dt, 4, base, dims, strides, box);
+}
+
+// Weights [256][K] K-major, (64, 256) box.
+cudaError_t encode_weights(CUtensorMap* map, DType dt, const void* base, int K) {
+  uint64_t dims[2] = {static_cast<uint64_t>(K), kTcBlockN};
+  uint64_t strides[1] = {static_cast<uint64_t>(K) * 2};
+  uint32_t box[2] = {kTcBlockK, kTcBlockN};
+  return encode(map, dt, 2, base, dims, strides, box);
+}
+
+bool valid_tiling(Conv3x3Tiling t) {
+  return t.tile_w >= 8 && t.tile_w <= 128 && (t.tile_w & (t.tile_w - 1)) == 0 &&
+         t.tile_w * t.tile_h == kTcBlockM;
+}
+
+void fill_tiling(TcGemmArgs& a, int N, int H, int W, Conv3x3Tiling t) {
+  a.N_img = N;
+  a.H = H;
+  a.W = W;
+  a.tile_w = t.tile_w;
+  a.tile_h = t.tile_h;
+  a.tiles_x = (W + t.tile_w - 1) / t.tile_w;
+  a.tiles_y = (H + t.tile_h - 1) / t.tile_h;
+}
+
 template <int kMode, typename T>
 cudaError_t launch_t(const TcPlan& p, cudaStream_t s) {
   static bool configured[64] = {};
@@ -69,13 +107,14 @@ cudaError_t launch_t(const TcPlan& p, cudaStream_t s) {
   if (dev < 64 && !configured[dev]) {
     cudaError_t e = cudaFuncSetAttribute(fpn_tc_gemm_kernel<kMode, T>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kTcSmemBytes);
+                                         TcCfg<kMode>::kSmemBytes);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
   TcGemmArgs a;
   std::memcpy(&a, p.args, sizeof(a));
-  fpn_tc_gemm_kernel<kMode, T><<<p.grid, kTcThreads, kTcSmemBytes, s>>>(p.map_a, p.map_b, a);
+  fpn_tc_gemm_kernel<kMode, T><<<p.grid, kTcThreads, TcCfg<kMode>::kSmemBytes, s>>>(
+      p.map_a, p.map_b, p.map_out, p.map_coarse, a);
   return cudaGetLastError();
 }
 
@@ -94,46 +133,67 @@ int sm_count() {
   return counts[dev];
 }
 
+Conv3x3Tiling default_tiling(int H, int W) {
+  Conv3x3Tiling best;
+  long long best_area = -1;
+  for (int tw : {16, 8, 32, 64, 128}) {
+    const int th = kTcBlockM / tw;
+    const long long area = static_cast<long long>((W + tw - 1) / tw) * tw *
+                           static_cast<long long>((H + th - 1) / th) * th;
+    if (best_area < 0 || area < best_area) {
+      best_area = area;
+      best.tile_w = tw;
+      best.tile_h = th;
+    }
+  }
+  return best;
+}
+
 cudaError_t plan_tc_lateral(TcPlan& plan, DType dt, const void* x, const void* w,
                             const float* bias, const void* coarse, void* out, int N, int Cin,
-                            int H, int W, int Hc, int Wc, int* status, int max_ctas) {
+                            int H, int W, int Hc, int Wc, Conv3x3Tiling tiling, int* status,
+                            int max_ctas) {
   if (dt != DType::BF16 && dt != DType::F16) return cudaErrorInvalidValue;
   if (Cin <= 0 || Cin % 8 != 0 || N <= 0 || H <= 0 || W <= 0) return cudaErrorInvalidValue;
+  if (!valid_tiling(tiling)) return cudaErrorInvalidValue;
+  if (coarse && (Hc <= 0 || Wc <= 0)) return cudaErrorInvalidValue;
   if (!aligned16(out) || (coarse && !aligned16(coarse)) || !aligned16(bias))
     return cudaErrorMisalignedAddress;
-  const long long M = static_cast<long long>(N) * H * W;
-  if (M >= (1LL << 31) - kTcBlockM) return cudaErrorInvalidValue;
-  const int esz = 2;
-  {
-    uint64_t dims[2] = {static_cast<uint64_t>(Cin), static_cast<uint64_t>(M)};
-    uint64_t strides[1] = {static_cast<uint64_t>(Cin) * esz};
-    uint32_t box[2] = {kTcBlockK, kTcBlockM};
-    cudaError_t e = encode(&plan.map_a, dt, 2, x, dims, strides, box);
-    if (e != cudaSuccess) return e;
-  }
-  {
-    uint64_t dims[2] = {static_cast<uint64_t>(Cin), kTcBlockN};
-    uint64_t strides[1] = {static_cast<uint64_t>(Cin) * esz};
-    uint32_t box[2] = {kTcBlockK, kTcBlockN};
-    cudaError_t e = encode(&plan.map_b, dt, 2, w, dims, strides, box);
-    if (e != cudaSuccess) return e;
-  }
   TcGemmArgs a;
   std::memset(&a, 0, sizeof(a));
-  a.num_tiles = static_cast<int>((M + kTcBlockM - 1) / kTcBlockM);
-  a.num_kb = (Cin + kTcBlockK - 1) / kTcBlockK;
-  a.M = static_cast<int>(M);
-  a.N_img = N;
-  a.H = H;
-  a.W = W;
+  fill_tiling(a, N, H, W, tiling);
+  const long long tiles = static_cast<long long>(a.tiles_x) * a.tiles_y * N;
+  if (tiles >= (1LL << 31)) return cudaErrorInvalidValue;
+  a.num_tiles = static_cast<int>(tiles);
+  a.cin_blocks = (Cin + kTcBlockK - 1) / kTcBlockK;
+  a.num_kb = a.cin_blocks;
   a.bias = bias;
-  a.out = out;
-  a.coarse = coarse;
-  a.Hc = Hc;
-  a.Wc = Wc;
-  a.scale_y = coarse ? static_cast<float>(Hc) / static_cast<float>(H) : 0.f;
-  a.scale_x = coarse ? static_cast<float>(Wc) / static_cast<float>(W) : 0.f;
   a.status = status;
+  cudaError_t e = encode_nhwc(&plan.map_a, dt, x, N, H, W, Cin, tiling.tile_w, tiling.tile_h);
+  if (e != cudaSuccess) return e;
+  if ((e = encode_weights(&plan.map_b, dt, w, Cin)) != cudaSuccess) return e;
+  const int sw = tiling.tile_w < 32 ? tiling.tile_w : 32;
+  if ((e = encode_nhwc(&plan.map_out, dt, out, N, H, W, kTcBlockN, sw, 32 / sw)) != cudaSuccess)
+    return e;
+  plan.map_coarse = plan.map_out;  // unused unless a coarse map is staged
+  if (coarse) {
+    a.coarse = coarse;
+    a.Hc = Hc;
+    a.Wc = Wc;
+    a.scale_y = static_cast<float>(Hc) / static_cast<float>(H);
+    a.scale_x = static_cast<float>(Wc) / static_cast<float>(W);
+    // Coarse rows/cols a tile's bilinear taps can touch: the span of the source
+    // coordinates of tile_h (tile_w) consecutive outputs plus the +1 neighbour.
+    const int ch = static_cast<int>(std::ceil((tiling.tile_h - 1) * a.scale_y)) + 2;
+    const int cw = static_cast<int>(std::ceil((tiling.tile_w - 1) * a.scale_x)) + 2;
+    if (ch * cw <= kTcCoarseMaxPix && ch <= 256 && cw <= 256) {
+      a.cbox_h = ch;
+      a.cbox_w = cw;
+      if ((e = encode_nhwc(&plan.map_coarse, dt, coarse, N, Hc, Wc, kTcBlockN, cw, ch)) !=
+          cudaSuccess)
+        return e;
+    }
+  }
   std::memcpy(plan.args, &a, sizeof(a));
   plan.mode = 0;
   plan.dtype = dt;
@@ -147,50 +207,31 @@ cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w
                             const float* bias, void* out, void* p6, int N, int H, int W,
                             Conv3x3Tiling tiling, int* status, int max_ctas) {
   if (dt != DType::BF16 && dt != DType::F16) return cudaErrorInvalidValue;
-  if (tiling.tile_w * tiling.tile_h != kTcBlockM || tiling.tile_w < 1 || tiling.tile_w > 128)
-    return cudaErrorInvalidValue;
+  if (!valid_tiling(tiling)) return cudaErrorInvalidValue;
   if (N <= 0 || H <= 0 || W <= 0) return cudaErrorInvalidValue;
   if (!aligned16(out) || (p6 && !aligned16(p6)) || !aligned16(bias))
     return cudaErrorMisalignedAddress;
   const int C = kTcBlockN;
-  const int esz = 2;
-  {
-    uint64_t dims[4] = {static_cast<uint64_t>(C), static_cast<uint64_t>(W),
-                        static_cast<uint64_t>(H), static_cast<uint64_t>(N)};
-    uint64_t strides[3] = {static_cast<uint64_t>(C) * esz, static_cast<uint64_t>(W) * C * esz,
-                           static_cast<uint64_t>(H) * W * C * esz};
-    uint32_t box[4] = {kTcBlockK, static_cast<uint32_t>(tiling.tile_w),
-                       static_cast<uint32_t>(tiling.tile_h), 1};
-    cudaError_t e = encode(&plan.map_a, dt, 4, x, dims, strides, box);
-    if (e != cudaSuccess) return e;
-  }
-  {
-    uint64_t dims[2] = {static_cast<uint64_t>(9 * C), kTcBlockN};
-    uint64_t strides[1] = {static_cast<uint64_t>(9 * C) * esz};
-    uint32_t box[2] = {kTcBlockK, kTcBlockN};
-    cudaError_t e = encode(&plan.map_b, dt, 2, w, dims, strides, box);
-    if (e != cudaSuccess) return e;
-  }
   TcGemmArgs a;
   std::memset(&a, 0, sizeof(a));
-  a.tile_w = tiling.tile_w;
-  a.tile_h = tiling.tile_h;
-  a.tiles_x = (W + tiling.tile_w - 1) / tiling.tile_w;
-  a.tiles_y = (H + tiling.tile_h - 1) / tiling.tile_h;
+  fill_tiling(a, N, H, W, tiling);
   const long long tiles = static_cast<long long>(a.tiles_x) * a.tiles_y * N;
   if (tiles >= (1LL << 31)) return cudaErrorInvalidValue;
   a.num_tiles = static_cast<int>(tiles);
   a.cin_blocks = C / kTcBlockK;
   a.num_kb = 9 * a.cin_blocks;
-  a.N_img = N;
-  a.H = H;
-  a.W = W;
   a.bias = bias;
-  a.out = out;
   a.p6 = p6;
   a.H6 = (H - 1) / 2 + 1;
   a.W6 = (W - 1) / 2 + 1;
   a.status = status;
+  cudaError_t e = encode_nhwc(&plan.map_a, dt, x, N, H, W, C, tiling.tile_w, tiling.tile_h);
+  if (e != cudaSuccess) return e;
+  if ((e = encode_weights(&plan.map_b, dt, w, 9 * C)) != cudaSuccess) return e;
+  const int sw = tiling.tile_w < 32 ? tiling.tile_w : 32;
+  if ((e = encode_nhwc(&plan.map_out, dt, out, N, H, W, kTcBlockN, sw, 32 / sw)) != cudaSuccess)
+    return e;
+  plan.map_coarse = plan.map_out;
   std::memcpy(plan.args, &a, sizeof(a));
   plan.mode = 1;
   plan.dtype = dt;

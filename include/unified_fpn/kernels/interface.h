@@ -57,11 +57,13 @@ struct Conv3x3Tiling {
 };
 
 // Everything one tensor-core launch needs, built on the host once per
-// (pointers, shapes) and replayable: the two TMA descriptors plus the
-// kernel argument block.
+// (pointers, shapes) and replayable: the TMA descriptors (A, B, output,
+// coarse map) plus the kernel argument block.
 struct TcPlan {
   alignas(64) CUtensorMap map_a;
   alignas(64) CUtensorMap map_b;
+  alignas(64) CUtensorMap map_out;
+  alignas(64) CUtensorMap map_coarse;
   unsigned char args[256];  // TcGemmArgs, opaque outside tc_kernels.cu
   int mode = 0;             // 0 lateral, 1 conv3x3
   DType dtype = DType::BF16;
@@ -74,12 +76,15 @@ struct TcPlan {
 //   coarse: NHWC [N][Hc][Wc][256] or null; out: NHWC [N][H][W][256].
 cudaError_t plan_tc_lateral(TcPlan& plan, DType dt, const void* x, const void* w,
                             const float* bias, const void* coarse, void* out, int N, int Cin,
-                            int H, int W, int Hc, int Wc, int* status, int max_ctas);
+                            int H, int W, int Hc, int Wc, Conv3x3Tiling tiling, int* status,
+                            int max_ctas);
 // 3x3 pad-1 conv, 256 -> 256: x NHWC [N][H][W][256]; w: [256][9][256]; out NHWC;
 // p6 (optional) NHWC [N][ceil(H/2)][ceil(W/2)][256].
 cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w,
                             const float* bias, void* out, void* p6, int N, int H, int W,
                             Conv3x3Tiling tiling, int* status, int max_ctas);
+// Tiling with the fewest padded pixels for an H x W map (ties: 16 wide).
+Conv3x3Tiling default_tiling(int H, int W);
 cudaError_t launch_tc(const TcPlan& plan, cudaStream_t s);
 
 // Number of SMs on the current device (cached).
