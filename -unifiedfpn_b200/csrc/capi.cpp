@@ -172,12 +172,34 @@ int ufpn_core_set_kernel_config(ufpn_core* core, int tile_size, int channels_per
                                 int use_tensor_cores, int activation, int enable_graph_capture) {
   if (!core) return fail(UFPN_ERR_INVALID_ARG, "NULL core");
   return guarded([&] {
-    FPNKernelConfig c;
+    FPNKernelConfig c = core->core.get_kernel_config();
     c.tile_size = tile_size;
     c.channels_per_thread = channels_per_thread;
     c.use_tensor_cores = use_tensor_cores != 0;
     c.activation = static_cast<FPNActivation>(activation);
     c.enable_graph_capture = enable_graph_capture != 0;
+    core->core.set_kernel_config(c);
+    return UFPN_OK;
+  });
+}
+
+int ufpn_core_trace_next_forward(ufpn_core* core) {
+  if (!core) return fail(UFPN_ERR_INVALID_ARG, "NULL core");
+  core->core.trace_next_forward();
+  return UFPN_OK;
+}
+
+int ufpn_core_get_neck_trace(const ufpn_core* core, unsigned long long* out8) {
+  if (!core || !out8) return fail(UFPN_ERR_INVALID_ARG, "NULL");
+  core->core.get_neck_trace(out8);
+  return UFPN_OK;
+}
+
+int ufpn_core_set_schedule(ufpn_core* core, int fused_neck_kernel) {
+  if (!core) return fail(UFPN_ERR_INVALID_ARG, "NULL core");
+  return guarded([&] {
+    FPNKernelConfig c = core->core.get_kernel_config();
+    c.fused_neck_kernel = fused_neck_kernel != 0;
     core->core.set_kernel_config(c);
     return UFPN_OK;
   });

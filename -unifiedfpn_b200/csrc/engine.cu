@@ -93,6 +93,10 @@ struct UnifiedFPNCore::Impl {
   size_t workspace_bytes = 0;
   size_t weight_bytes = 0;
   int* d_status = nullptr;
+  int* d_sched = nullptr;  // neck-kernel tile counter + level completion counters
+  unsigned long long* d_trace = nullptr;  // neck-kernel timeline (same allocation)
+  bool trace_next = false;
+  unsigned long long last_trace[8] = {};
   cudaStream_t side = nullptr;
   cudaStream_t capture = nullptr;
   cudaStream_t setup = nullptr;
@@ -155,6 +159,7 @@ struct UnifiedFPNCore::Impl {
     free_weights();
     cudaFree(d_status);
     d_status = nullptr;
+    d_sched = nullptr;  // same allocation
     if (side) cudaStreamDestroy(side);
     if (capture) cudaStreamDestroy(capture);
     if (setup) cudaStreamDestroy(setup);
@@ -262,6 +267,38 @@ struct UnifiedFPNCore::Impl {
         x[l] = nhwc_in[l];
       }
     }
+    if (cfg.fused_neck_kernel && !prof_events) {
+      ufpn::NeckLevel lv[4];
+      for (int l = 0; l < 4; ++l) {
+        lv[l].x = x[l];
+        lv[l].lat_w = lat_wp[l];
+        lv[l].lat_b = lat_b[l];
+        lv[l].conv_w = out_wp[l];
+        lv[l].conv_b = out_b[l];
+        lv[l].merged = merged[l];
+        lv[l].out = o[l];
+        lv[l].Cin = cin[l];
+        lv[l].H = H[l];
+        lv[l].W = W[l];
+        lv[l].lat_tiling = ufpn::default_tiling(H[l], W[l]);
+        lv[l].conv_tiling = tiling_for(l);
+      }
+      ufpn::NeckPlan plan;
+      check(ufpn::plan_neck(plan, dtype, batch, lv, o6, d_sched, d_status, 0,
+                            trace_next ? d_trace : nullptr),
+            "plan neck");
+      ok(ufpn::launch_neck(plan, main), "neck launch");
+      if (nchw) {
+        for (int l = 0; l < 4; ++l)
+          ok(ufpn::launch_transpose(dtype, o[l], out[l], batch, cout, H[l] * W[l], false, main),
+             "NHWC->NCHW");
+        if (p6)
+          ok(ufpn::launch_transpose(dtype, o6, p6, batch, cout,
+                                    ((H[3] - 1) / 2 + 1) * ((W[3] - 1) / 2 + 1), false, main),
+             "NHWC->NCHW");
+      }
+      return launches;
+    }
     cudaStream_t conv_stream = prof_events ? main : side;
     if (!prof_events) {
       check(cudaEventRecord(ev_fork, main), "event");
@@ -337,8 +374,10 @@ UnifiedFPNCore::UnifiedFPNCore(size_t workspace_size, int device) : impl_(new Im
   CUDA_CHECK(cudaEventCreateWithFlags(&impl_->ev_join, cudaEventDisableTiming));
   for (auto& e : impl_->ev_lat) CUDA_CHECK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   for (auto& e : impl_->prof) CUDA_CHECK(cudaEventCreate(&e));
-  CUDA_CHECK(cudaMalloc(&impl_->d_status, 256));
-  CUDA_CHECK(cudaMemset(impl_->d_status, 0, 256));
+  CUDA_CHECK(cudaMalloc(&impl_->d_status, 1024));
+  CUDA_CHECK(cudaMemset(impl_->d_status, 0, 1024));
+  impl_->d_sched = impl_->d_status + 64;
+  impl_->d_trace = reinterpret_cast<unsigned long long*>(impl_->d_status + 128);
 }
 
 UnifiedFPNCore::~UnifiedFPNCore() = default;
@@ -497,6 +536,18 @@ void UnifiedFPNCore::forward_raw(const void* const* in, void* const* out, void* 
     m.profiling = false;
     return;
   }
+  if (m.trace_next) {
+    // One directly launched forward with the neck kernel's timeline recorded.
+    m.check(cudaMemsetAsync(m.d_trace, 0, 8 * sizeof(unsigned long long), stream), "memset");
+    m.check(cudaMemsetAsync(m.d_trace, 0xFF, sizeof(unsigned long long), stream), "memset");
+    m.metrics.num_kernel_launches = m.enqueue(in, out, p6, stream, false);
+    m.check(cudaMemcpyAsync(m.last_trace, m.d_trace, sizeof(m.last_trace),
+                            cudaMemcpyDeviceToHost, stream),
+            "trace copy");
+    m.check(cudaStreamSynchronize(stream), "trace sync");
+    m.trace_next = false;
+    return;
+  }
   if (m.cfg.enable_graph_capture) {
     for (auto& e : m.graphs) {
       if (e.p6 != p6) continue;
@@ -580,11 +631,19 @@ void UnifiedFPNCore::set_kernel_config(const FPNKernelConfig& config) {
   impl_->cfg = config;
 }
 
+FPNKernelConfig UnifiedFPNCore::get_kernel_config() const { return impl_->cfg; }
+
 size_t UnifiedFPNCore::get_memory_usage() const {
   return impl_->workspace_bytes + impl_->weight_bytes;
 }
 
 void UnifiedFPNCore::set_profiling(bool enable) { impl_->profiling = enable; }
+
+void UnifiedFPNCore::trace_next_forward() { impl_->trace_next = true; }
+
+void UnifiedFPNCore::get_neck_trace(unsigned long long* out8) const {
+  std::memcpy(out8, impl_->last_trace, sizeof(impl_->last_trace));
+}
 
 int UnifiedFPNCore::device_status(bool reset) {
   DeviceGuard g(impl_->device);
@@ -592,6 +651,8 @@ int UnifiedFPNCore::device_status(bool reset) {
   CUDA_CHECK(cudaDeviceSynchronize());
   CUDA_CHECK(cudaMemcpy(&v, impl_->d_status, sizeof(int), cudaMemcpyDeviceToHost));
   if (reset) CUDA_CHECK(cudaMemset(impl_->d_status, 0, sizeof(int)));
+  // After a pipeline abort, make sure the neck kernel's schedule counters start at zero.
+  if (reset && v != 0) CUDA_CHECK(cudaMemset(impl_->d_sched, 0, 64 * sizeof(int)));
   return v;
 }
 

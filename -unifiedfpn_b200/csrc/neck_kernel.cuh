@@ -1,0 +1,612 @@
+// The whole tensor-core FPN neck in ONE persistent kernel launch.
+//
+// The neck is 8 implicit-GEMM jobs over 128-pixel x 256-channel tiles:
+//   lat5, lat4, conv5(+P6), lat3, conv4, lat2, conv3, conv2
+// (lat_l = 1x1 lateral + bias [+ bilinear(M_{l+1}) when l < 5], conv_l = 3x3 pad-1 + bias).
+// Reference schedule: UnifiedFPNCore::forward, lib/core/fpn_engine.cu:191-245
+// (lateral loop, then top-down loop P5 -> P2); semantics as in tc_gemm.cuh.
+//
+// Tiles are numbered job by job in the order above and handed out by a global
+// atomic counter (dynamic scheduling).  Data dependencies are enforced on the
+// device with per-level completion counters:
+//   * a conv_l tile's producer waits until every lat_l tile has been stored
+//     before it loads M_l (its 3x3 halo crosses tile borders);
+//   * a lat_l tile's epilogue waits until every lat_{l+1} tile has been stored
+//     before it reads M_{l+1} for the bilinear taps.
+// Because a tile only ever waits for tiles with smaller numbers, and tiles are
+// taken in increasing order by CTAs that are already running, every wait is
+// for work that a resident CTA has taken: the schedule cannot deadlock, even
+// if not all CTAs are resident.  Every wait is still bounded (ptx.cuh).
+//
+// Cross-CTA visibility: an epilogue waits for its own TMA stores to complete
+// (cp.async.bulk.wait_group 0), fences the async proxy, synchronises the
+// epilogue warps and publishes with a release add; consumers acquire the
+// counter and fence the async proxy before issuing TMA loads.
+//
+// Roles per CTA (one CTA per SM):
+//   warp 0 lane 0 : tile fetcher + TMA producer
+//   warp 1        : TMEM allocator; lane 0 issues tcgen05.mma
+//   warps 2..9    : epilogue (TMEM -> bias / bilinear -> smem -> TMA store);
+//                   warp 2 lane 0 also loads the staged coarse box
+// The fetched tile id is passed to the MMA and epilogue roles through a small
+// shared-memory ring guarded by mbarriers.
+#pragma once
+
+#include "tc_gemm.cuh"
+
+namespace ufpn {
+
+constexpr int kNeckMaxJobs = 8;
+constexpr int kNeckRing = 4;
+constexpr int kNeckStages = 3;
+
+struct NeckJob {
+  CUtensorMap map_a;       // activations (NHWC, 4-D box (64, tile_w, tile_h, 1))
+  CUtensorMap map_b;       // weights [256][K]
+  CUtensorMap map_out;     // output (NHWC, box (64, min(tile_w,32), 32/.., 1))
+  CUtensorMap map_coarse;  // lateral: M_{l+1} (NHWC, box (64, cbox_w, cbox_h, 1))
+  int mode;                // 0 lateral, 1 conv3x3
+  int level;               // 0..3 = P2..P5
+  int tile_start;          // first global tile number
+  int num_tiles;
+  int num_kb;
+  int cin_blocks;
+  int N_img, H, W;
+  int tile_w, tile_h, tiles_x, tiles_y;
+  const float* bias;
+  const void* coarse;      // lateral with top-down add
+  int Hc, Wc;
+  float scale_y, scale_x;
+  int cbox_w, cbox_h;
+  void* p6;
+  int H6, W6;
+  int dep_level;           // level whose laterals must be complete (-1: none)
+  int dep_count;           // number of tiles of that lateral job
+};
+
+struct NeckParams {
+  NeckJob jobs[kNeckMaxJobs];
+  int num_jobs;
+  int total_tiles;
+  int lat_tiles[4];  // lateral tiles per level (completion targets)
+  int* sched;   // [0] tile counter, [1 + l] completed lateral tiles of level l, [7] exit counter
+  int* status;  // device status word
+  // Optional timeline (globaltimer ns): [0] first CTA start (min), [1 + l] time level l's
+  // laterals completed, [5] last CTA end (max), [6] first conv2 tile MMA start (min).
+  unsigned long long* trace;
+};
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ int atom_release_gpu_add(int* p, int v) {
+  int old;
+  asm volatile("atom.release.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
+               : "memory");
+  return old;
+}
+__device__ __forceinline__ void fence_proxy_async_all() {
+  asm volatile("fence.proxy.async;" ::: "memory");
+}
+__device__ __forceinline__ void epi_bar_sync() {
+  asm volatile("bar.sync 1, %0;" ::"r"(kTcEpiWarps * 32) : "memory");
+}
+// Named barrier over the epilogue warps that also ANDs a predicate: every
+// epilogue thread gets the same answer, so exits taken on it are uniform and no
+// warp is ever left waiting at a later bar.sync for one that left.
+__device__ __forceinline__ bool epi_vote_all(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 q, %1, 0;\n\t"
+      "bar.red.and.pred p, 1, %2, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "r"(kTcEpiWarps * 32)
+      : "memory");
+  return r != 0;
+}
+
+// Bounded wait until *counter >= target (acquire).  Returns false on timeout/abort.
+__device__ __forceinline__ bool wait_counter(const int* counter, int target,
+                                             volatile int* abort_flag, int* status, int code) {
+  if (ld_acquire_gpu(counter) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i) {
+      __nanosleep(64);
+      if (ld_acquire_gpu(counter) >= target) return true;
+    }
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+      *abort_flag = 1;
+      if (status) atomicCAS(status, 0, code);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ int neck_find_job(const NeckParams& p, int t) {
+  int j = 0;
+#pragma unroll 1
+  for (int k = 1; k < p.num_jobs; ++k)
+    if (t >= p.jobs[k].tile_start) j = k;
+  return j;
+}
+
+__device__ __forceinline__ void neck_tile_origin(const NeckJob& jb, int local, int& n, int& x0,
+                                                 int& y0) {
+  const int tx = local % jb.tiles_x;
+  const int t2 = local / jb.tiles_x;
+  const int ty = t2 % jb.tiles_y;
+  n = t2 / jb.tiles_y;
+  x0 = tx * jb.tile_w;
+  y0 = ty * jb.tile_h;
+}
+
+constexpr int kNeckOffB = kNeckStages * kTcAStage;
+constexpr int kNeckOffStaging = kNeckOffB + kNeckStages * kTcBStage;
+constexpr int kNeckCoarseBlk = kTcCoarseMaxPix * 128;
+constexpr int kNeckOffCoarse = kNeckOffStaging + kTcEpiWarps * kTcStagingPerWarp;
+constexpr int kNeckOffBars = kNeckOffCoarse + 4 * kNeckCoarseBlk;
+constexpr int kNeckSmemBytes = kNeckOffBars + 512 + 1024;
+static_assert(kNeckSmemBytes <= 232448, "neck smem");
+
+constexpr int kDevTimeoutDependency = 0x105;
+
+template <typename T>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    fpn_neck_kernel(const __grid_constant__ NeckParams P) {
+  constexpr int S = kNeckStages;
+  constexpr int R = kNeckRing;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint8_t* smem_a = smem;
+  uint8_t* smem_b = smem + kNeckOffB;
+  uint8_t* smem_stage = smem + kNeckOffStaging;
+  uint8_t* smem_coarse = smem + kNeckOffCoarse;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kNeckOffBars);
+  uint64_t* full_bar = bars;
+  uint64_t* empty_bar = bars + S;
+  uint64_t* accf_bar = bars + 2 * S;
+  uint64_t* acce_bar = accf_bar + 2;
+  uint64_t* done_bar = acce_bar + 2;
+  uint64_t* cfull_bar = done_bar + 1;
+  uint64_t* rfull_bar = cfull_bar + 1;
+  uint64_t* rempty_bar = rfull_bar + R;
+  int* ring = reinterpret_cast<int*>(rempty_bar + R);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ring + R);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  int* sched = P.sched;
+
+  if (threadIdx.x == 0) {
+    if (P.trace) atomicMin(&P.trace[0], globaltimer_ns());
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf_bar[b], 1);
+      mbar_init(&acce_bar[b], kTcEpiWarps * 32);
+    }
+    mbar_init(done_bar, 1);
+    mbar_init(cfull_bar, 1);
+    for (int r = 0; r < R; ++r) {
+      mbar_init(&rfull_bar[r], 1);
+      mbar_init(&rempty_bar[r], 1 + kTcEpiWarps);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTcTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ fetcher + TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int rslot = 0;
+      uint32_t rphase = 0;
+      int issued = 0;
+      bool ok = true;
+      int ready_level_mask = 0;  // dependency levels already observed complete
+      // The next tile number is fetched one tile ahead so the atomic's round trip
+      // overlaps the current tile's loads instead of stalling between tiles.
+      int t_next = atomicAdd(&sched[0], 1);
+      while (ok) {
+        const int t = t_next;
+        if (t < P.total_tiles) t_next = atomicAdd(&sched[0], 1);
+        if (!mbar_wait(&rempty_bar[rslot], rphase ^ 1u, abort_flag, P.status,
+                       kDevTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        ring[rslot] = t < P.total_tiles ? t : -1;
+        mbar_arrive(&rfull_bar[rslot]);
+        if (++rslot == R) {
+          rslot = 0;
+          rphase ^= 1u;
+        }
+        if (t >= P.total_tiles) break;
+        const int j = neck_find_job(P, t);
+        const NeckJob& jb = P.jobs[j];
+        int n, x0, y0;
+        neck_tile_origin(jb, t - jb.tile_start, n, x0, y0);
+        if (jb.mode == 1 && jb.dep_level >= 0 && !(ready_level_mask & (1 << jb.dep_level))) {
+          if (!wait_counter(&sched[1 + jb.dep_level], jb.dep_count, abort_flag, P.status,
+                            kDevTimeoutDependency)) {
+            ok = false;
+            break;
+          }
+          fence_proxy_async_all();
+          ready_level_mask |= 1 << jb.dep_level;
+        }
+        for (int kb = 0; kb < jb.num_kb; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, P.status,
+                         kDevTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full_bar[stage], kTcAStage + kTcBStage);
+          int dy = 0, dx = 0, cb = kb;
+          if (jb.mode == 1) {
+            const int tap = kb / jb.cin_blocks;
+            cb = kb - tap * jb.cin_blocks;
+            dy = tap / 3 - 1;
+            dx = tap % 3 - 1;
+          }
+          tma_load_4d(smem_a + stage * kTcAStage, &jb.map_a, &full_bar[stage], cb * kTcBlockK,
+                      x0 + dx, y0 + dy, n, jb.mode == 0 ? kPolicyEvictFirst : kPolicyEvictLast);
+          tma_load_2d(smem_b + stage * kTcBStage, &jb.map_b, &full_bar[stage], kb * kTcBlockK, 0,
+                      kPolicyEvictLast);
+          ++issued;
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Unblock the consumers: publish an end marker if a ring slot is free.
+        if (mbar_test(smem_u32(&rempty_bar[rslot]), rphase ^ 1u)) {
+          ring[rslot] = -1;
+          mbar_arrive(&rfull_bar[rslot]);
+        }
+      }
+      for (int i = 0; i < S && i < issued; ++i) {
+        if (--stage < 0) {
+          stage = S - 1;
+          phase ^= 1u;
+        }
+        mbar_wait_drain(&full_bar[stage], phase);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc(kTcBlockM, kTcBlockN, Pack<T>::kFmt, Pack<T>::kFmt);
+      int stage = 0;
+      uint32_t phase = 0;
+      int rslot = 0;
+      uint32_t rphase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      while (ok) {
+        if (!mbar_wait(&rfull_bar[rslot], rphase, abort_flag, P.status, kDevTimeoutMma)) break;
+        const int t = ring[rslot];
+        mbar_arrive(&rempty_bar[rslot]);
+        if (++rslot == R) {
+          rslot = 0;
+          rphase ^= 1u;
+        }
+        if (t < 0) break;
+        const NeckJob& jm = P.jobs[neck_find_job(P, t)];
+        const int num_kb = jm.num_kb;
+        if (P.trace && jm.mode == 1 && jm.level == 0 && t == jm.tile_start)
+          P.trace[6] = globaltimer_ns();
+        if (!mbar_wait(&acce_bar[acc], acc_phase ^ 1u, abort_flag, P.status, kDevTimeoutMma))
+          break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kTcBlockN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag, P.status, kDevTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = sdesc_kmajor_sw128(smem_u32(smem_a + stage * kTcAStage));
+          const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(smem_b + stage * kTcBStage));
+#pragma unroll
+          for (int k = 0; k < kTcBlockK / 16; ++k)
+            tc_mma_f16(d_tmem, adesc + 2u * k, bdesc + 2u * k, idesc,
+                       (kb > 0 || k > 0) ? 1u : 0u);
+          tc_commit(&empty_bar[stage]);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&accf_bar[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      tc_commit(done_bar);
+      mbar_wait_drain(done_bar, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp - 2;
+    const int quarter = warp & 3;
+    const int chalf = ew >> 2;
+    const int row = quarter * 32 + lane;
+    const bool leader = (ew == 0) && (lane == 0);  // issues the coarse box loads
+    const uint32_t stage_addr = smem_u32(smem_stage + ew * kTcStagingPerWarp);
+    const uint32_t coarse_addr = smem_u32(smem_coarse);
+    int rslot = 0;
+    uint32_t rphase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    uint32_t cphase = 0;
+    int coarse_requested = -1;  // leader: tile whose coarse box is in flight / resident
+    int ready_level_mask = 0;   // leader: dependency levels observed complete
+    bool ok = true;
+
+    // Leader: make sure level `lvl` laterals are complete (acquire), then load the
+    // coarse box of lateral tile `t` of job `jb`.
+    auto request_coarse = [&](const NeckJob& jb, int t) -> bool {
+      if (!(ready_level_mask & (1 << (jb.level + 1)))) {
+        if (!wait_counter(&sched[1 + jb.level + 1], jb.dep_count, abort_flag, P.status,
+                          kDevTimeoutDependency))
+          return false;
+        fence_proxy_async_all();
+        ready_level_mask |= 1 << (jb.level + 1);
+      }
+      if (jb.cbox_w > 0) {
+        int n, x0, y0;
+        neck_tile_origin(jb, t - jb.tile_start, n, x0, y0);
+        const int cy = static_cast<int>(tc_src(y0, jb.scale_y, jb.Hc));
+        const int cx = static_cast<int>(tc_src(x0, jb.scale_x, jb.Wc));
+        mbar_arrive_expect_tx(cfull_bar, static_cast<uint32_t>(jb.cbox_w * jb.cbox_h * 128 * 4));
+        for (int b = 0; b < 4; ++b)
+          tma_load_4d(smem_coarse + b * kNeckCoarseBlk, &jb.map_coarse, cfull_bar, b * 64, cx,
+                      cy, n, kPolicyEvictLast);
+      }
+      coarse_requested = t;
+      return true;
+    };
+
+    while (true) {
+      const bool got =
+          mbar_wait(&rfull_bar[rslot], rphase, abort_flag, P.status, kDevTimeoutEpilogue);
+      const int t = got ? ring[rslot] : -1;
+      __syncwarp();
+      if (lane == 0 && got) mbar_arrive(&rempty_bar[rslot]);
+      if (++rslot == R) {
+        rslot = 0;
+        rphase ^= 1u;
+      }
+      if (!epi_vote_all(got && ok) || t < 0) break;  // uniform: same ring slot for all
+      const NeckJob& jb = P.jobs[neck_find_job(P, t)];
+      const bool lateral = jb.mode == 0;
+      const bool has_coarse = lateral && jb.coarse != nullptr;
+      const bool staged = has_coarse && jb.cbox_w > 0;
+      if (has_coarse && leader && coarse_requested != t) ok = request_coarse(jb, t);
+      bool wok = mbar_wait(&accf_bar[acc], acc_phase, abort_flag, P.status, kDevTimeoutEpilogue);
+      if (staged && wok && ok)
+        wok = mbar_wait(cfull_bar, cphase, abort_flag, P.status, kDevTimeoutEpilogue);
+      // Uniform exit; the barrier also orders the leader's acquire of the coarse
+      // level before every thread's global-memory taps (unstaged path).
+      if (!epi_vote_all(wok && ok)) break;
+      tc_fence_after();
+
+      int n, x0, y0;
+      neck_tile_origin(jb, t - jb.tile_start, n, x0, y0);
+      const int tw = jb.tile_w;
+      const int py = y0 + row / tw;
+      const int px = x0 + row % tw;
+      const bool valid = (py < jb.H) && (px < jb.W);
+
+      float w00 = 0.f, w01 = 0.f, w10 = 0.f, w11 = 0.f;
+      int r00 = 0, r01 = 0, r10 = 0, r11 = 0;
+      bool corners_staged = false;
+      const uint8_t* g00 = nullptr;
+      const uint8_t* g01 = nullptr;
+      const uint8_t* g10 = nullptr;
+      const uint8_t* g11 = nullptr;
+      if (has_coarse) {
+        const float sy = tc_src(min(py, jb.H - 1), jb.scale_y, jb.Hc);
+        const float sx = tc_src(min(px, jb.W - 1), jb.scale_x, jb.Wc);
+        const int ya = static_cast<int>(sy);
+        const int xa = static_cast<int>(sx);
+        const int yb = min(ya + 1, jb.Hc - 1);
+        const int xb = min(xa + 1, jb.Wc - 1);
+        const float wy = sy - static_cast<float>(ya);
+        const float wx = sx - static_cast<float>(xa);
+        w00 = (1.f - wy) * (1.f - wx);
+        w01 = (1.f - wy) * wx;
+        w10 = wy * (1.f - wx);
+        w11 = wy * wx;
+        if (staged) {
+          const int cy0 = static_cast<int>(tc_src(y0, jb.scale_y, jb.Hc));
+          const int cx0 = static_cast<int>(tc_src(x0, jb.scale_x, jb.Wc));
+          corners_staged = (ya - cy0) >= 0 && (yb - cy0) < jb.cbox_h && (xa - cx0) >= 0 &&
+                           (xb - cx0) < jb.cbox_w;
+          r00 = (ya - cy0) * jb.cbox_w + (xa - cx0);
+          r01 = (ya - cy0) * jb.cbox_w + (xb - cx0);
+          r10 = (yb - cy0) * jb.cbox_w + (xa - cx0);
+          r11 = (yb - cy0) * jb.cbox_w + (xb - cx0);
+        }
+        if (!corners_staged) {
+          const size_t rowb = static_cast<size_t>(kTcBlockN) * sizeof(T);
+          const uint8_t* cbase = static_cast<const uint8_t*>(jb.coarse) +
+                                 static_cast<size_t>(n) * jb.Hc * jb.Wc * rowb;
+          g00 = cbase + (static_cast<size_t>(ya) * jb.Wc + xa) * rowb;
+          g01 = cbase + (static_cast<size_t>(ya) * jb.Wc + xb) * rowb;
+          g10 = cbase + (static_cast<size_t>(yb) * jb.Wc + xa) * rowb;
+          g11 = cbase + (static_cast<size_t>(yb) * jb.Wc + xb) * rowb;
+        }
+      }
+      const bool emit_p6 =
+          (!lateral) && (jb.p6 != nullptr) && valid && ((py & 1) == 0) && ((px & 1) == 0);
+      uint8_t* p6_row = nullptr;
+      if (emit_p6) {
+        const size_t p6pix = (static_cast<size_t>(n) * jb.H6 + (py >> 1)) * jb.W6 + (px >> 1);
+        p6_row = static_cast<uint8_t*>(jb.p6) + p6pix * kTcBlockN * sizeof(T);
+      }
+      const int wrow0 = quarter * 32;
+      const int ox = x0 + (wrow0 % tw);
+      const int oy = y0 + wrow0 / tw;
+
+#pragma unroll 1
+      for (int step = 0; step < 2; ++step) {
+        const int col0 = chalf * 128 + step * 64;
+        uint32_t r[64];
+        __syncwarp();
+        const uint32_t taddr = tmem_base + static_cast<uint32_t>(acc * kTcBlockN + col0) +
+                               (static_cast<uint32_t>(quarter * 32) << 16);
+        tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        tmem_ld32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+        tmem_wait_ld();
+        if (step == 1) {
+          tc_fence_before();
+          mbar_arrive(&acce_bar[acc]);
+        }
+        float v[64];
+        const float4* b4 = reinterpret_cast<const float4*>(jb.bias + col0);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float4 bb = __ldg(b4 + i);
+          v[4 * i + 0] = __uint_as_float(r[4 * i + 0]) + bb.x;
+          v[4 * i + 1] = __uint_as_float(r[4 * i + 1]) + bb.y;
+          v[4 * i + 2] = __uint_as_float(r[4 * i + 2]) + bb.z;
+          v[4 * i + 3] = __uint_as_float(r[4 * i + 3]) + bb.w;
+        }
+        if (has_coarse) {
+          const int blk = col0 >> 6;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            uint4 a, b, c, d;
+            if (corners_staged) {
+              const uint32_t base = coarse_addr + blk * kNeckCoarseBlk;
+              a = ld_shared_v4(base + r00 * 128 + ((j ^ (r00 & 7)) << 4));
+              b = ld_shared_v4(base + r01 * 128 + ((j ^ (r01 & 7)) << 4));
+              c = ld_shared_v4(base + r10 * 128 + ((j ^ (r10 & 7)) << 4));
+              d = ld_shared_v4(base + r11 * 128 + ((j ^ (r11 & 7)) << 4));
+            } else {
+              // Written by other CTAs during this launch: L2-coherent loads (ld.global.cg),
+              // never the non-coherent / L1-cached read-only path.
+              const size_t off = static_cast<size_t>(col0) * sizeof(T);
+              a = __ldcg(reinterpret_cast<const uint4*>(g00 + off) + j);
+              b = __ldcg(reinterpret_cast<const uint4*>(g01 + off) + j);
+              c = __ldcg(reinterpret_cast<const uint4*>(g10 + off) + j);
+              d = __ldcg(reinterpret_cast<const uint4*>(g11 + off) + j);
+            }
+            const uint32_t au[4] = {a.x, a.y, a.z, a.w};
+            const uint32_t bu[4] = {b.x, b.y, b.z, b.w};
+            const uint32_t cu[4] = {c.x, c.y, c.z, c.w};
+            const uint32_t du[4] = {d.x, d.y, d.z, d.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 fa = Pack<T>::unpack(au[e]);
+              const float2 fb = Pack<T>::unpack(bu[e]);
+              const float2 fc = Pack<T>::unpack(cu[e]);
+              const float2 fd = Pack<T>::unpack(du[e]);
+              v[8 * j + 2 * e + 0] += w00 * fa.x + w01 * fb.x + w10 * fc.x + w11 * fd.x;
+              v[8 * j + 2 * e + 1] += w00 * fa.y + w01 * fb.y + w10 * fc.y + w11 * fd.y;
+            }
+          }
+        }
+        if (lane == 0) bulk_wait_group_read<0>();
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          uint4 o;
+          o.x = Pack<T>::pack(v[8 * j + 0], v[8 * j + 1]);
+          o.y = Pack<T>::pack(v[8 * j + 2], v[8 * j + 3]);
+          o.z = Pack<T>::pack(v[8 * j + 4], v[8 * j + 5]);
+          o.w = Pack<T>::pack(v[8 * j + 6], v[8 * j + 7]);
+          st_shared_v4(stage_addr + lane * 128 + ((j ^ (lane & 7)) << 4), o);
+          if (emit_p6)
+            reinterpret_cast<uint4*>(p6_row + static_cast<size_t>(col0) * sizeof(T))[j] = o;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_4d(&jb.map_out, smem_stage + ew * kTcStagingPerWarp, col0, ox, oy, n);
+          bulk_commit_group();
+        }
+      }
+      if (staged) cphase ^= 1u;
+      if (lateral) {
+        // Publish the tile: own stores complete -> all epilogue warps -> one release add.
+        if (lane == 0) {
+          bulk_wait_group<0>();
+          fence_proxy_async_all();
+          __threadfence();
+        }
+        __syncwarp();
+        epi_bar_sync();  // also: every warp is done reading this tile's coarse box
+        if (leader) {
+          const int before = atom_release_gpu_add(&sched[1 + jb.level], 1);
+          if (P.trace && before + 1 == P.lat_tiles[jb.level])
+            P.trace[1 + jb.level] = globaltimer_ns();
+        }
+      }
+      // The coarse buffer is free (lateral tiles passed the barrier above; other
+      // tiles do not read it): prefetch the next tile's coarse box if that tile is
+      // a lateral with a top-down add.
+      if (leader && ok) {
+        if (mbar_wait(&rfull_bar[rslot], rphase, abort_flag, P.status, kDevTimeoutEpilogue)) {
+          const int tn = ring[rslot];
+          if (tn >= 0) {
+            const NeckJob& jn = P.jobs[neck_find_job(P, tn)];
+            if (jn.mode == 0 && jn.coarse != nullptr) ok = request_coarse(jn, tn);
+          }
+        }
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTcTmemCols);
+  }
+  if (threadIdx.x == 0) {
+    if (P.trace) atomicMax(&P.trace[5], globaltimer_ns());
+    // The last CTA to leave resets the schedule counters for the next launch.
+    __threadfence();
+    if (atomicAdd(&sched[7], 1) == static_cast<int>(gridDim.x) - 1) {
+      for (int i = 0; i < 8; ++i) sched[i] = 0;
+      __threadfence();
+    }
+  }
+}
+
+}  // namespace ufpn

@@ -7,6 +7,7 @@
 #include <mutex>
 
 #include "kernels.h"
+#include "neck_kernel.cuh"
 #include "tc_gemm.cuh"
 
 namespace ufpn {
@@ -239,6 +240,139 @@ cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w
   const int cap = max_ctas > 0 ? max_ctas : sm_count();
   plan.grid = a.num_tiles < cap ? a.num_tiles : cap;
   return cudaSuccess;
+}
+
+static_assert(sizeof(NeckParams) <= sizeof(NeckPlan::params), "NeckPlan::params too small");
+
+cudaError_t plan_neck(NeckPlan& plan, DType dt, int N, const NeckLevel* lv, void* p6,
+                      int* sched, int* status, int max_ctas, unsigned long long* trace) {
+  if (dt != DType::BF16 && dt != DType::F16) return cudaErrorInvalidValue;
+  if (N <= 0 || !sched) return cudaErrorInvalidValue;
+  NeckParams* P = reinterpret_cast<NeckParams*>(plan.params);
+  std::memset(plan.params, 0, sizeof(plan.params));
+  int lat_tiles[4] = {};
+  for (int l = 0; l < 4; ++l) {
+    const NeckLevel& L = lv[l];
+    if (!valid_tiling(L.lat_tiling) || !valid_tiling(L.conv_tiling)) return cudaErrorInvalidValue;
+    if (L.Cin <= 0 || L.Cin % 8 != 0 || L.H <= 0 || L.W <= 0) return cudaErrorInvalidValue;
+    if (!aligned16(L.merged) || !aligned16(L.out) || !aligned16(L.lat_b) || !aligned16(L.conv_b))
+      return cudaErrorMisalignedAddress;
+    lat_tiles[l] = ((L.W + L.lat_tiling.tile_w - 1) / L.lat_tiling.tile_w) *
+                   ((L.H + L.lat_tiling.tile_h - 1) / L.lat_tiling.tile_h) * N;
+  }
+  // Dispatch order: each job only depends on jobs before it.  All laterals go first:
+  // their main loops depend on nothing, so every SM can work on them while the
+  // top-down chain (lat5 -> lat4 -> lat3 -> lat2 epilogues) resolves; the 3x3 tiles,
+  // the bulk of the FLOPs, follow and fill the machine.
+  const int order[8][2] = {{0, 3}, {0, 2}, {0, 1}, {0, 0}, {1, 3}, {1, 2}, {1, 1}, {1, 0}};
+  int start = 0;
+  for (int j = 0; j < 8; ++j) {
+    const int mode = order[j][0], l = order[j][1];
+    const NeckLevel& L = lv[l];
+    NeckJob& J = P->jobs[j];
+    J.mode = mode;
+    J.level = l;
+    const Conv3x3Tiling t = mode == 0 ? L.lat_tiling : L.conv_tiling;
+    J.N_img = N;
+    J.H = L.H;
+    J.W = L.W;
+    J.tile_w = t.tile_w;
+    J.tile_h = t.tile_h;
+    J.tiles_x = (L.W + t.tile_w - 1) / t.tile_w;
+    J.tiles_y = (L.H + t.tile_h - 1) / t.tile_h;
+    J.num_tiles = J.tiles_x * J.tiles_y * N;
+    J.tile_start = start;
+    start += J.num_tiles;
+    J.dep_level = -1;
+    cudaError_t e;
+    const int sw = t.tile_w < 32 ? t.tile_w : 32;
+    if (mode == 0) {
+      J.cin_blocks = (L.Cin + kTcBlockK - 1) / kTcBlockK;
+      J.num_kb = J.cin_blocks;
+      J.bias = L.lat_b;
+      if ((e = encode_nhwc(&J.map_a, dt, L.x, N, L.H, L.W, L.Cin, t.tile_w, t.tile_h)) != cudaSuccess)
+        return e;
+      if ((e = encode_weights(&J.map_b, dt, L.lat_w, L.Cin)) != cudaSuccess) return e;
+      if ((e = encode_nhwc(&J.map_out, dt, L.merged, N, L.H, L.W, kTcBlockN, sw, 32 / sw)) !=
+          cudaSuccess)
+        return e;
+      J.map_coarse = J.map_out;
+      if (l < 3) {
+        const NeckLevel& C = lv[l + 1];
+        J.coarse = C.merged;
+        J.Hc = C.H;
+        J.Wc = C.W;
+        J.scale_y = static_cast<float>(C.H) / static_cast<float>(L.H);
+        J.scale_x = static_cast<float>(C.W) / static_cast<float>(L.W);
+        J.dep_count = lat_tiles[l + 1];
+        const int ch = static_cast<int>(std::ceil((t.tile_h - 1) * J.scale_y)) + 2;
+        const int cw = static_cast<int>(std::ceil((t.tile_w - 1) * J.scale_x)) + 2;
+        if (ch * cw <= kTcCoarseMaxPix && ch <= 256 && cw <= 256) {
+          J.cbox_h = ch;
+          J.cbox_w = cw;
+          if ((e = encode_nhwc(&J.map_coarse, dt, C.merged, N, C.H, C.W, kTcBlockN, cw, ch)) !=
+              cudaSuccess)
+            return e;
+        }
+      }
+    } else {
+      J.cin_blocks = kTcBlockN / kTcBlockK;
+      J.num_kb = 9 * J.cin_blocks;
+      J.bias = L.conv_b;
+      J.dep_level = l;
+      J.dep_count = lat_tiles[l];
+      if ((e = encode_nhwc(&J.map_a, dt, L.merged, N, L.H, L.W, kTcBlockN, t.tile_w,
+                           t.tile_h)) != cudaSuccess)
+        return e;
+      if ((e = encode_weights(&J.map_b, dt, L.conv_w, 9 * kTcBlockN)) != cudaSuccess) return e;
+      if ((e = encode_nhwc(&J.map_out, dt, L.out, N, L.H, L.W, kTcBlockN, sw, 32 / sw)) !=
+          cudaSuccess)
+        return e;
+      J.map_coarse = J.map_out;
+      if (l == 3 && p6) {
+        if (!aligned16(p6)) return cudaErrorMisalignedAddress;
+        J.p6 = p6;
+        J.H6 = (L.H - 1) / 2 + 1;
+        J.W6 = (L.W - 1) / 2 + 1;
+      }
+    }
+  }
+  P->num_jobs = 8;
+  P->total_tiles = start;
+  for (int l = 0; l < 4; ++l) P->lat_tiles[l] = lat_tiles[l];
+  P->trace = trace;
+  P->sched = sched;
+  P->status = status;
+  plan.dtype = dt;
+  plan.total_tiles = start;
+  const int cap = max_ctas > 0 ? max_ctas : sm_count();
+  plan.grid = start < cap ? start : cap;
+  return cudaSuccess;
+}
+
+namespace {
+template <typename T>
+cudaError_t launch_neck_t(const NeckPlan& p, cudaStream_t s) {
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(fpn_neck_kernel<T>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kNeckSmemBytes);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  const NeckParams* P = reinterpret_cast<const NeckParams*>(p.params);
+  fpn_neck_kernel<T><<<p.grid, kTcThreads, kNeckSmemBytes, s>>>(*P);
+  return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t launch_neck(const NeckPlan& plan, cudaStream_t s) {
+  if (plan.grid <= 0) return cudaSuccess;
+  return plan.dtype == DType::BF16 ? launch_neck_t<__nv_bfloat16>(plan, s)
+                                   : launch_neck_t<__half>(plan, s);
 }
 
 cudaError_t launch_tc(const TcPlan& plan, cudaStream_t s) {

@@ -233,6 +233,24 @@ class UnifiedFPN:
         check(lib.ufpn_core_set_kernel_config(self._h, tile_size, channels_per_thread, int(use_tensor_cores),
                                               _ACT[activation], int(enable_graph_capture)), "set_kernel_config")
 
+    def set_schedule(self, fused_neck_kernel: bool = False) -> None:
+        """Tensor-core schedule: one persistent kernel for the whole neck, or eight
+        per-level kernels on two streams (default).  Results are bitwise identical."""
+        check(lib.ufpn_core_set_schedule(self._h, int(fused_neck_kernel)), "set_schedule")
+
+    def neck_timeline(self, backbone_features) -> dict:
+        """Runs one forward with the fused neck kernel's device timeline recorded and
+        returns microseconds since the kernel started: when each level's laterals were
+        complete, when the first P2 3x3 tile started, and the end."""
+        check(lib.ufpn_core_trace_next_forward(self._h), "trace_next_forward")
+        self.forward(backbone_features, return_p6=True)
+        tr = (ctypes.c_ulonglong * 8)()
+        check(lib.ufpn_core_get_neck_trace(self._h, tr), "get_neck_trace")
+        t0 = tr[0]
+        us = lambda v: (v - t0) / 1e3 if v else None  # noqa: E731
+        return {"lat_P5_done": us(tr[4]), "lat_P4_done": us(tr[3]), "lat_P3_done": us(tr[2]),
+                "lat_P2_done": us(tr[1]), "conv_P2_first_tile": us(tr[6]), "end": us(tr[5])}
+
     def get_memory_usage(self) -> int:
         return int(lib.ufpn_core_get_memory_usage(self._h))
 

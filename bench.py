@@ -196,6 +196,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-roofline", action="store_true")
+    ap.add_argument("--schedule", choices=["fused", "split"], default="split",
+                    help="one persistent neck kernel, or eight per-level kernels on two streams")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
@@ -228,6 +230,7 @@ def main():
                       .to(dtype).contiguous(memory_format=torch.channels_last)
                       for c, (h, w) in zip(R50_CHANNELS, sizes)])
     fpn = U.UnifiedFPN(device=dev)
+    fpn.set_schedule(fused_neck_kernel=args.schedule == "fused")
     outs = []
     for s in range(n_sets):
         o = fpn(feats[s], return_p6=True)
@@ -350,6 +353,11 @@ def main():
         roofline["neck_frac_of_roofline"] = round(t_roof * 1e3 / ms_per_step, 4)
         roofline["neck_roofline_ms"] = round(t_roof * 1e3, 4)
 
+    timeline = None
+    if args.schedule == "fused" and not args.no_roofline:
+        timeline = {k: (round(v, 1) if v is not None else None)
+                    for k, v in fpn.neck_timeline(feats[0]).items()}
+
     cpu = None
     if rank == 0 and not args.no_cpu_baseline and world == 1:
         cpu = cpu_baseline()
@@ -366,6 +374,7 @@ def main():
                        "l2": f"inputs rotate over {n_sets} sets (~{n_sets * 117} MB at 800x1216 b2) > 126 MB L2",
                        "parallelism": f"dp{world} batch shards, no collective on the data path"},
             "clocks": clk, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
+            "schedule": args.schedule, "neck_timeline_us": timeline,
             "roofline": roofline, "kernel_time_share": kernel_share, "cpu_baseline": cpu,
             "device_status": status,
         }

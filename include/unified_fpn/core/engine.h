@@ -48,11 +48,17 @@ class __attribute__((visibility("default"))) UnifiedFPNCore {
 
   const FPNPerformanceMetrics& get_performance_metrics() const;
   void set_kernel_config(const FPNKernelConfig& config);
+  FPNKernelConfig get_kernel_config() const;
   size_t get_memory_usage() const;
 
   // Time every kernel of the next forward() with CUDA events (serialises the
   // schedule; synchronises the stream at the end of that forward).
   void set_profiling(bool enable);
+  // Record the fused neck kernel's device timeline during the next forward() (launched
+  // directly, then the stream is synchronised).  get_neck_trace returns globaltimer ns:
+  // [0] start, [1..4] P2..P5 laterals complete, [5] end, [6] first P2 3x3 tile started.
+  void trace_next_forward();
+  void get_neck_trace(unsigned long long* out8) const;
   // Measure the candidate tilings of every level with the given buffers and keep
   // the fastest; returns a human-readable report.
   std::string autotune(const void* const* inputs, void* const* outputs, void* p6,

@@ -134,6 +134,10 @@ struct FPNKernelConfig {
   bool enable_async_copy = true; // TMA is always used on the tensor-core path
   FPNActivation activation = FPNActivation::NONE;
   bool enable_graph_capture = true;  // replay the P5->P2 schedule as one CUDA graph
+  // Tensor-core path: run all 4 laterals and 4 3x3 convs as ONE persistent kernel with
+  // device-side level dependencies (true), or as 8 kernels on two streams (false, the
+  // faster schedule at the R50 800x1216 batch-2 workload today).
+  bool fused_neck_kernel = false;
 };
 
 struct FPNWeights {

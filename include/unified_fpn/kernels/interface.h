@@ -85,6 +85,33 @@ cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w
                             Conv3x3Tiling tiling, int* status, int max_ctas);
 // Tiling with the fewest padded pixels for an H x W map (ties: 16 wide).
 Conv3x3Tiling default_tiling(int H, int W);
+
+// ---- whole-neck persistent kernel (one launch for all 4 laterals and 4 3x3 convs)
+struct NeckLevel {
+  const void* x;        // C_l, NHWC [N][H][W][Cin]
+  const void* lat_w;    // [256][Cin] in the compute dtype
+  const float* lat_b;   // [256]
+  const void* conv_w;   // [256][9][256] in the compute dtype
+  const float* conv_b;  // [256]
+  void* merged;         // M_l workspace, NHWC [N][H][W][256]
+  void* out;            // P_l, NHWC [N][H][W][256]
+  int Cin, H, W;
+  Conv3x3Tiling lat_tiling, conv_tiling;
+};
+struct NeckPlan {
+  alignas(64) unsigned char params[6144];  // NeckParams, opaque outside tc_kernels.cu
+  DType dtype = DType::BF16;
+  int grid = 0;
+  int total_tiles = 0;
+};
+// levels[0..3] = P2..P5; p6 (NHWC, optional) = P5[::2, ::2].  sched: 8 device ints,
+// zero before the first launch (each launch leaves them zero again).
+// trace (optional, 8 device u64): [0] = ~0 and the rest 0 before the launch; receives the
+// launch's timeline in globaltimer ns (see NeckParams in neck_kernel.cuh).
+cudaError_t plan_neck(NeckPlan& plan, DType dt, int N, const NeckLevel* levels, void* p6,
+                      int* sched, int* status, int max_ctas,
+                      unsigned long long* trace = nullptr);
+cudaError_t launch_neck(const NeckPlan& plan, cudaStream_t s);
 cudaError_t launch_tc(const TcPlan& plan, cudaStream_t s);
 
 // Number of SMs on the current device (cached).

@@ -77,6 +77,10 @@ int ufpn_core_forward(ufpn_core* core, const void* const* inputs, void* const* o
  * FPNActivation ordinal (only NONE is supported). */
 int ufpn_core_set_kernel_config(ufpn_core* core, int tile_size, int channels_per_thread,
                                 int use_tensor_cores, int activation, int enable_graph_capture);
+/* Tensor-core schedule: 1 = one persistent kernel for the whole neck, 0 = eight kernels on
+ * two streams (default).  No reference counterpart (its engine launched 16 kernels on four
+ * unordered streams, fpn_engine.cu:191-245). */
+int ufpn_core_set_schedule(ufpn_core* core, int fused_neck_kernel);
 /* fpn_engine.cu:408-415 (get_memory_usage) */
 size_t ufpn_core_get_memory_usage(const ufpn_core* core);
 /* fpn_pytorch.cpp:171-187 (get_performance_breakdown): kernel_times_ms[8], metrics[5] =
@@ -85,6 +89,11 @@ int ufpn_core_get_performance_metrics(const ufpn_core* core, float* kernel_times
                                       float* metrics);
 /* Time each kernel of the next forward with events (serialised). */
 int ufpn_core_set_profiling(ufpn_core* core, int enable);
+/* Record the fused neck kernel's device timeline during the next forward (synchronises);
+ * out8 (globaltimer ns): [0] start, [1..4] P2..P5 laterals complete, [5] end,
+ * [6] first P2 3x3 tile started.  No reference counterpart. */
+int ufpn_core_trace_next_forward(ufpn_core* core);
+int ufpn_core_get_neck_trace(const ufpn_core* core, unsigned long long* out8);
 /* lib/utils/auto_tuner.cu:213-275 (auto_tune_lateral_conv), for every level of the neck. */
 int ufpn_core_autotune(ufpn_core* core, const void* const* inputs, void* const* outputs,
                        void* p6, void* stream, int iterations);

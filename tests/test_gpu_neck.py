@@ -82,6 +82,30 @@ def test_neck_r50_800x1216_batch2_full_size(cuda_device):
         assert torch.equal(a, b)
 
 
+@pytest.mark.parametrize("geom", [(O.R50_CHANNELS, O.level_sizes(128, 192), 2),
+                                  (O.SWIN_CHANNELS, [(100, 167), (50, 84), (25, 42), (13, 21)], 1),
+                                  (O.R50_CHANNELS, O.level_sizes(800, 1216), 2)])
+def test_fused_neck_kernel_matches_per_level_kernels(cuda_device, geom):
+    """The single persistent neck kernel (device-side level dependencies) and the eight
+    per-level kernels compute every tile identically: outputs must be bitwise equal."""
+    import unified_fpn as U
+    chans, sizes, batch = geom
+    feats = [_cl(f.to(torch.bfloat16).cuda()) for f in O.make_features(batch, chans, sizes, seed=33)]
+    fpn = U.UnifiedFPN()
+    fused = _run(fpn, feats)
+    assert fpn.device_status() == 0
+    fpn.set_schedule(fused_neck_kernel=False)
+    split = _run(fpn, feats)
+    for a, b in zip(fused, split):
+        assert torch.equal(a, b)
+    fpn.set_schedule(fused_neck_kernel=True)
+    for _ in range(3):  # repeated launches: the schedule counters must reset themselves
+        again = _run(fpn, feats)
+        for a, b in zip(fused, again):
+            assert torch.equal(a, b)
+    assert fpn.device_status() == 0
+
+
 def test_neck_batch_linearity_and_sharding(cuda_device):
     """Images are independent: the neck on a batch equals the neck on each slice
     (the property multi-GPU batch sharding relies on)."""
