@@ -94,6 +94,10 @@ int guarded(F&& f) {
 
 }  // namespace
 
+namespace ufpn {
+void set_last_error(const std::string& msg) { g_last_error = msg; }
+}  // namespace ufpn
+
 extern "C" {
 
 const char* ufpn_last_error(void) { return g_last_error.c_str(); }

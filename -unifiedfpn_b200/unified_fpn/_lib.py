@@ -75,6 +75,10 @@ SIGNATURES = {
                 c_void_p]),
     "ufpn_p6_maxpool": (c_int, [c_int, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
     "ufpn_pack_conv3x3_weights": (c_int, [c_int, c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "ufpn_neck_forward_noalloc": (
+        c_int, [c_int, POINTER(c_void_p), POINTER(c_void_p), POINTER(c_void_p), POINTER(c_void_p),
+                POINTER(c_void_p), POINTER(c_void_p), c_void_p, c_int, POINTER(c_int), POINTER(c_int),
+                POINTER(c_int), c_void_p, c_void_p]),
     "ufpn_convert_weights": (c_int, [c_int, c_void_p, c_void_p, c_longlong, c_void_p]),
     "ufpn_layout_convert": (c_int, [c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p]),
     "launch_production_upsample_float": (

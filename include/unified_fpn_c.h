@@ -136,6 +136,28 @@ int ufpn_upsample_add(int dtype, int layout, const void* coarse, const void* lat
 int ufpn_p6_maxpool(int dtype, int layout, const void* p5, void* p6, int N, int C, int H, int W,
                     void* stream);
 
+/* The whole tensor-core neck (P2..P5 and optional P6) in one call that allocates nothing.
+ * No counterpart in the reference: it exists for callers that cannot call cudaMalloc on
+ * their hot path (servers that own all device memory through a fixed arena, real-time
+ * loops that must not enter the driver's allocator, code embedded in a framework that
+ * must not create untracked allocations).
+ *   inputs: C2..C5, NHWC, dtype BF16/F16; lateral_w[l]: [256][Cin_l] and output_w[l]:
+ *   [256][9][256] (ufpn_pack_conv3x3_weights) in the same dtype; biases fp32 [256];
+ *   outputs: P2..P5 NHWC; p6 NHWC or NULL; status: optional caller-owned device int that
+ *   receives a pipeline-timeout code (NULL = internal).
+ * Scratch (merged maps M2..M5 = batch * sum(H_l * W_l) * 512 bytes, plus 512 bytes of
+ * counters) lives in a file-scope device array of UFPN_NOALLOC_SCRATCH_BYTES that every
+ * GPU loading the library holds until exit; larger problems are rejected with
+ * UFPN_ERR_INVALID_ARG.  The first call on a device looks the array's address up
+ * (cudaGetSymbolAddress) and should come before any stream capture.  All calls share the
+ * array: each clears the counters it needs, and calls that overlap on the GPU race. */
+#define UFPN_NOALLOC_SCRATCH_BYTES (64u << 20)
+int ufpn_neck_forward_noalloc(int dtype, const void* const* inputs,
+                              const void* const* lateral_w, const float* const* lateral_b,
+                              const void* const* output_w, const float* const* output_b,
+                              void* const* outputs, void* p6, int batch, const int* in_channels,
+                              const int* heights, const int* widths, int* status, void* stream);
+
 /* fp32 [Cout][Cin][3][3] (device) -> dtype [Cout][9][Cin] K-major packing for ufpn_conv3x3. */
 int ufpn_pack_conv3x3_weights(int dtype, const float* w, void* out, int Cout, int Cin,
                               void* stream);
