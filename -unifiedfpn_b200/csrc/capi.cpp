@@ -319,14 +319,15 @@ int ufpn_conv3x3(int dtype, const void* x, const void* w, const float* bias, voi
   if (!ufpn::aligned16(x) || !ufpn::aligned16(w) || !ufpn::aligned16(out) ||
       !ufpn::aligned16(bias) || (p6 && !ufpn::aligned16(p6)))
     return fail(UFPN_ERR_ALIGNMENT, "tensors must be 16-byte aligned");
-  ufpn::Conv3x3Tiling t;
+  ufpn::Conv3x3Tiling t = ufpn::halo_tiling();  // tile_w == 0: halo reuse, 8 x 16 tiles
   if (tile_w > 0) {
     if (tile_w > 128 || 128 % tile_w != 0)
       return fail(UFPN_ERR_INVALID_ARG, "tile_w must be 8, 16, 32, 64 or 128");
     t.tile_w = tile_w;
     t.tile_h = 128 / tile_w;
-  } else {
-    t = ufpn::default_tiling(H, W);
+    t.halo = false;
+  } else if (tile_w < 0) {
+    return fail(UFPN_ERR_INVALID_ARG, "tile_w must be 0 (halo tiling) or 8..128");
   }
   int* status = device_status_word();
   ufpn::TcPlan plan;

@@ -60,9 +60,15 @@ DType to_dtype(FPNDataType t) {
   }
 }
 
-// Heuristic 3x3 tiling: the tile_w in {8..128} that wastes the fewest padded
-// pixels (ties go to 16, then to the wider tile).
-Conv3x3Tiling heuristic_tiling(int H, int W) { return ufpn::default_tiling(H, W); }
+// 3x3 tiling from its tuning code: 0 = halo reuse with 8 x 16 tiles (the default),
+// 8..128 = plain tiles of that width (one shifted box per tap).
+Conv3x3Tiling tiling_from_code(int tw) {
+  if (tw <= 0) return ufpn::halo_tiling();
+  Conv3x3Tiling t;
+  t.tile_w = tw;
+  t.tile_h = 128 / tw;
+  return t;
+}
 
 }  // namespace
 
@@ -304,15 +310,29 @@ struct UnifiedFPNCore::Impl {
       check(cudaEventRecord(ev_fork, main), "event");
       check(cudaStreamWaitEvent(side, ev_fork, 0), "event");
     }
-    for (int l = 3; l >= 0; --l) {
-      TcPlan lat;
-      check(ufpn::plan_tc_lateral(lat, dtype, x[l], lat_wp[l], lat_b[l],
-                                  l < 3 ? merged[l + 1] : nullptr, merged[l], batch, cin[l], H[l],
-                                  W[l], l < 3 ? H[l + 1] : 0, l < 3 ? W[l + 1] : 0,
-                                  ufpn::default_tiling(H[l], W[l]), d_status, 0),
-            "plan lateral");
-      ok(ufpn::launch_tc(lat, main), "lateral launch");
-      if (prof_events) cudaEventRecord(prof[1 + 2 * (3 - l)], main);
+    // Main stream (the top-down data dependence):
+    //   1. ONE grouped launch of the raw P5, P4, P3 laterals L5, L4, L3 (as GEMMs they do
+    //      not depend on one another; only their top-down adds chain);
+    //   2. in-place merges M4 = L4 + up(M5), M3 = L3 + up(M4) (bandwidth kernels on the
+    //      small maps; M5 = L5);
+    //   3. the P2 lateral with the top-down add of M3 fused into its epilogue.
+    // Side stream: each level's 3x3 as soon as its merged map exists.
+    ufpn::NeckLevel lv[4];
+    for (int l = 0; l < 4; ++l) {
+      lv[l].x = x[l];
+      lv[l].lat_w = lat_wp[l];
+      lv[l].lat_b = lat_b[l];
+      lv[l].conv_w = out_wp[l];
+      lv[l].conv_b = out_b[l];
+      lv[l].merged = merged[l];
+      lv[l].out = o[l];
+      lv[l].Cin = cin[l];
+      lv[l].H = H[l];
+      lv[l].W = W[l];
+      lv[l].lat_tiling = ufpn::default_tiling(H[l], W[l]);
+      lv[l].conv_tiling = tiling_for(l);
+    }
+    auto conv_level = [&](int l) {
       if (!prof_events) {
         check(cudaEventRecord(ev_lat[l], main), "event");
         check(cudaStreamWaitEvent(side, ev_lat[l], 0), "event");
@@ -323,8 +343,32 @@ struct UnifiedFPNCore::Impl {
                                   d_status, 0),
             "plan conv3x3");
       ok(ufpn::launch_tc(conv, conv_stream), "conv3x3 launch");
-      if (prof_events) cudaEventRecord(prof[2 + 2 * (3 - l)], main);
+    };
+    const ufpn::NeckJobSpec grouped[3] = {{0, 3, 0}, {0, 2, 0}, {0, 1, 0}};
+    ufpn::NeckPlan gplan;
+    check(ufpn::plan_neck_jobs(gplan, dtype, batch, lv, nullptr, grouped, 3, d_sched, d_status, 0),
+          "plan grouped laterals");
+    ok(ufpn::launch_neck(gplan, main), "grouped laterals launch");
+    if (prof_events) cudaEventRecord(prof[1], main);
+    conv_level(3);
+    if (prof_events) cudaEventRecord(prof[2], main);
+    for (int l = 2; l >= 1; --l) {
+      ok(ufpn::launch_upsample_add(dtype, merged[l + 1], merged[l], merged[l], batch, cout,
+                                   H[l + 1], W[l + 1], H[l], W[l], 0, Layout::NHWC, main),
+         "merge");
+      if (prof_events) cudaEventRecord(prof[3 + 2 * (2 - l)], main);
+      conv_level(l);
+      if (prof_events) cudaEventRecord(prof[4 + 2 * (2 - l)], main);
     }
+    TcPlan lat2;
+    check(ufpn::plan_tc_lateral(lat2, dtype, x[0], lat_wp[0], lat_b[0], merged[1], merged[0],
+                                batch, cin[0], H[0], W[0], H[1], W[1], lv[0].lat_tiling, d_status,
+                                0),
+          "plan lateral");
+    ok(ufpn::launch_tc(lat2, main), "lateral launch");
+    if (prof_events) cudaEventRecord(prof[7], main);
+    conv_level(0);
+    if (prof_events) cudaEventRecord(prof[8], main);
     if (nchw) {
       for (int l = 0; l < 4; ++l)
         ok(ufpn::launch_transpose(dtype, o[l], out[l], batch, cout, H[l] * W[l], false,
@@ -418,12 +462,11 @@ void UnifiedFPNCore::configure_levels(const std::vector<FPNDimensions>& dims, in
     m.cin[l] = dims[l].channels;
     m.H[l] = dims[l].height;
     m.W[l] = dims[l].width;
-    m.tiling[l] = heuristic_tiling(m.H[l], m.W[l]);
+    m.tiling[l] = ufpn::halo_tiling();
     m.tiling_tuned[l] = false;
     auto it = m.tuning_db.find(m.tuning_key(l));
     if (it != m.tuning_db.end()) {
-      m.tiling[l].tile_w = it->second.first;
-      m.tiling[l].tile_h = 128 / it->second.first;
+      m.tiling[l] = tiling_from_code(it->second.first);
       m.tiling_tuned[l] = true;
     }
   }
@@ -675,12 +718,10 @@ std::string UnifiedFPNCore::autotune(const void* const* in, void* const* out, vo
   if (iterations < 1) iterations = 1;
   for (int l = 3; l >= 0; --l) {
     float best_ms = -1.f;
-    int best_tw = m.tiling[l].tile_w;
-    for (int tw : {8, 16, 32, 64, 128}) {
+    int best_tw = m.tiling[l].halo ? 0 : m.tiling[l].tile_w;
+    for (int tw : {0, 8, 16, 32, 64, 128}) {  // 0 = halo reuse, 8 x 16 tiles
       if (tw > 2 * m.W[l] && tw != 8) continue;  // wider than the image: pure padding
-      Conv3x3Tiling t;
-      t.tile_w = tw;
-      t.tile_h = 128 / tw;
+      const Conv3x3Tiling t = tiling_from_code(tw);
       TcPlan conv;
       const bool nchw = m.layout == Layout::NCHW;
       void* o = nchw ? m.nhwc_out[l] : out[l];
@@ -696,17 +737,18 @@ std::string UnifiedFPNCore::autotune(const void* const* in, void* const* out, vo
       cudaEventElapsedTime(&ms, m.prof[0], m.prof[1]);
       ms /= iterations;
       rep << "P" << (l + 2) << " 3x3 " << m.batch << "x" << m.H[l] << "x" << m.W[l] << " tile "
-          << tw << "x" << 128 / tw << ": " << ms * 1e3 << " us\n";
+          << t.tile_w << "x" << t.tile_h << (t.halo ? " halo" : "") << ": " << ms * 1e3
+          << " us\n";
       if (best_ms < 0 || ms < best_ms) {
         best_ms = ms;
         best_tw = tw;
       }
     }
-    m.tiling[l].tile_w = best_tw;
-    m.tiling[l].tile_h = 128 / best_tw;
+    m.tiling[l] = tiling_from_code(best_tw);
     m.tiling_tuned[l] = true;
     m.tuning_db[m.tuning_key(l)] = {best_tw, best_ms};
-    rep << "P" << (l + 2) << " -> tile " << best_tw << "x" << 128 / best_tw << "\n";
+    rep << "P" << (l + 2) << " -> tile " << m.tiling[l].tile_w << "x" << m.tiling[l].tile_h
+        << (m.tiling[l].halo ? " halo" : "") << "\n";
   }
   m.release_graphs();
   if (device_status(true) != 0) FPN_THROW("device pipeline timeout during autotuning");
@@ -733,15 +775,14 @@ bool UnifiedFPNCore::load_tuning(const std::string& path) {
   int tw;
   float ms;
   while (f >> key >> tw >> ms) {
-    if (tw > 0 && tw <= 128 && 128 % tw == 0) impl_->tuning_db[key] = {tw, ms};
+    if (tw == 0 || (tw >= 8 && tw <= 128 && 128 % tw == 0)) impl_->tuning_db[key] = {tw, ms};
   }
   Impl& m = *impl_;
   if (m.configured) {
     for (int l = 0; l < 4; ++l) {
       auto it = m.tuning_db.find(m.tuning_key(l));
       if (it != m.tuning_db.end()) {
-        m.tiling[l].tile_w = it->second.first;
-        m.tiling[l].tile_h = 128 / it->second.first;
+        m.tiling[l] = tiling_from_code(it->second.first);
         m.tiling_tuned[l] = true;
       }
     }

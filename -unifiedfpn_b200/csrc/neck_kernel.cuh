@@ -62,6 +62,7 @@ struct NeckJob {
   int H6, W6;
   int dep_level;           // level whose laterals must be complete (-1: none)
   int dep_count;           // number of tiles of that lateral job
+  int publish;             // lateral: a later job of this launch waits on this level
 };
 
 struct NeckParams {
@@ -555,7 +556,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
       if (staged) cphase ^= 1u;
-      if (lateral) {
+      if (lateral && jb.publish) {
         // Publish the tile: own stores complete -> all epilogue warps -> one release add.
         if (lane == 0) {
           bulk_wait_group<0>();
@@ -569,6 +570,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if (P.trace && before + 1 == P.lat_tiles[jb.level])
             P.trace[1 + jb.level] = globaltimer_ns();
         }
+      } else if (staged) {
+        epi_bar_sync();  // every warp is done reading this tile's coarse box
       }
       // The coarse buffer is free (lateral tiles passed the barrier above; other
       // tiles do not read it): prefetch the next tile's coarse box if that tile is

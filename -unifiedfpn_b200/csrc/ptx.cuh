@@ -250,13 +250,29 @@ __device__ __forceinline__ uint64_t sdesc_kmajor_sw128(uint32_t saddr) {
   return d;
 }
 
-// Instruction descriptor for kind::f16 / kind::f8f6f4 with fp32 accumulation,
-// both operands K-major.  a_fmt/b_fmt: kind::f16 -> 0 = f16, 1 = bf16;
-// kind::f8f6f4 -> 0 = e4m3, 1 = e5m2.
-__host__ __device__ constexpr uint32_t make_idesc(int M, int N, uint32_t a_fmt, uint32_t b_fmt) {
+// Shared-memory matrix descriptor for an MN-major 16-bit operand with the 128-byte
+// swizzle: rows along K of 128 B (64 consecutive M/N elements), 8-row swizzle atoms
+// of 1024 B stacked along K (stride-dimension offset 1024 B), successive 64-element
+// M/N chunks `chunk_stride` bytes apart (leading-dimension offset).  Advancing K by 16
+// is +2048 bytes on the start address.  Base must be 1024-byte aligned.
+__device__ __forceinline__ uint64_t sdesc_mnmajor_sw128(uint32_t saddr, uint32_t chunk_stride) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);            // start address  [0,14)
+  d |= static_cast<uint64_t>((chunk_stride >> 4) & 0x3FFFu) << 16; // leading offset [16,30)
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;                     // stride offset  [32,46)
+  d |= static_cast<uint64_t>(1) << 46;                             // version (sm_100)
+  d |= static_cast<uint64_t>(2) << 61;                             // 128-byte swizzle
+  return d;
+}
+
+// Instruction descriptor for kind::f16 / kind::f8f6f4 with fp32 accumulation.
+// a_fmt/b_fmt: kind::f16 -> 0 = f16, 1 = bf16; kind::f8f6f4 -> 0 = e4m3, 1 = e5m2.
+// b_mn_major: B stored MN-major (N contiguous) instead of K-major.
+__host__ __device__ constexpr uint32_t make_idesc(int M, int N, uint32_t a_fmt, uint32_t b_fmt,
+                                                  uint32_t b_mn_major = 0) {
   return (1u << 4)                                // D format: f32
          | (a_fmt << 7) | (b_fmt << 10)           // A / B formats
-         | (0u << 15) | (0u << 16)                // A, B K-major
+         | (0u << 15) | (b_mn_major << 16)        // A K-major, B K- or MN-major
          | (static_cast<uint32_t>(N >> 3) << 17)  // N / 8
          | (static_cast<uint32_t>(M >> 4) << 24); // M / 16
 }

@@ -81,52 +81,135 @@ struct Vec16 {
 };
 
 // ---------------------------------------------------------------- NHWC upsample-add
-// out[n,y,x,c] = lat[n,y,x,c] (or 0) + bilinear(coarse)[n,y,x,c].  One thread per
-// 16-byte channel vector; consecutive threads walk channels of one pixel, so every
-// load and store of a warp is a contiguous, fully coalesced 512-byte segment.
+// out[n,y,x,c] = lat[n,y,x,c] (or 0) + bilinear(coarse)[n,y,x,c].
+// A block takes one output row segment of 32 pixels: the row's vertical taps are
+// computed once per block; warp w takes pixels x0 + 4w .. x0 + 4w + 3 and first issues
+// all of their loads (4 coarse corners + the lateral, 16 bytes per lane each, every one a
+// contiguous 512-byte segment per warp for C = 256 16-bit channels) and only then does
+// the math and the stores, so each warp keeps 20 independent loads in flight and the
+// per-pixel index arithmetic is a handful of 32-bit operations.  `out` may alias `lat`
+// (in-place merge M_l = L_l + up(M_{l+1})): every element is read, then written, by the
+// same lane.
+constexpr int kUpPix = 4;  // pixels per warp
 template <typename T, bool kVec>
 __global__ void __launch_bounds__(256) upsample_add_nhwc_kernel(
-    const T* __restrict__ coarse, const T* __restrict__ lat, T* __restrict__ out, int N, int C,
-    int Hc, int Wc, int H, int W, float sy_scale, float sx_scale, int ac) {
+    const T* __restrict__ coarse, const T* lat, T* out, int N, int C, int Hc, int Wc, int H,
+    int W, float sy_scale, float sx_scale, int ac) {
   constexpr int V = kVec ? Vec16<T>::kN : 1;
-  const int cv_per_pix = C / V;
-  const long long total = static_cast<long long>(N) * H * W * cv_per_pix;
-  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int cv = static_cast<int>(i % cv_per_pix);
-    const long long pix = i / cv_per_pix;
-    const int x = static_cast<int>(pix % W);
-    const long long t = pix / W;
-    const int y = static_cast<int>(t % H);
-    const int n = static_cast<int>(t / H);
-    const BilinearTap tp = make_tap(y, x, Hc, Wc, H, W, sy_scale, sx_scale, ac);
-    const size_t cbase = static_cast<size_t>(n) * Hc * Wc;
-    const size_t i00 = (cbase + static_cast<size_t>(tp.y0) * Wc + tp.x0) * C + cv * V;
-    const size_t i01 = (cbase + static_cast<size_t>(tp.y0) * Wc + tp.x1) * C + cv * V;
-    const size_t i10 = (cbase + static_cast<size_t>(tp.y1) * Wc + tp.x0) * C + cv * V;
-    const size_t i11 = (cbase + static_cast<size_t>(tp.y1) * Wc + tp.x1) * C + cv * V;
-    const size_t io = static_cast<size_t>(pix) * C + cv * V;
-    if constexpr (kVec) {
-      Vec16<T> a, b, c, d, l, o;
-      a.u = __ldg(reinterpret_cast<const uint4*>(coarse + i00));
-      b.u = __ldg(reinterpret_cast<const uint4*>(coarse + i01));
-      c.u = __ldg(reinterpret_cast<const uint4*>(coarse + i10));
-      d.u = __ldg(reinterpret_cast<const uint4*>(coarse + i11));
-      if (lat) l.u = __ldg(reinterpret_cast<const uint4*>(lat + io));
+  const int cvs = C / V;  // channel vectors per pixel
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int segs = (W + 8 * kUpPix - 1) / (8 * kUpPix);
+  const int units = N * H * segs;
+  for (int u = blockIdx.x; u < units; u += gridDim.x) {
+    const int r = u / segs;
+    const int xb = (u - r * segs) * (8 * kUpPix) + warp * kUpPix;
+    if (xb >= W) continue;
+    const int n = r / H;
+    const int y = r - n * H;
+    const float sy = src_coord(y, Hc, H, sy_scale, ac);
+    const int y0 = static_cast<int>(sy);
+    const int y1 = min(y0 + 1, Hc - 1);
+    const float wy = sy - static_cast<float>(y0);
+    const T* c0 = coarse + (static_cast<size_t>(n) * Hc + y0) * Wc * C;
+    const T* c1 = coarse + (static_cast<size_t>(n) * Hc + y1) * Wc * C;
+    T* orow = out + static_cast<size_t>(r) * W * C;
+    const T* lrow = lat ? lat + static_cast<size_t>(r) * W * C : nullptr;
+    for (int cv = lane; cv < cvs; cv += 32) {
+      const int e0 = cv * V;
+      if constexpr (kVec) {
+        Vec16<T> a[kUpPix], b[kUpPix], c[kUpPix], d[kUpPix], l[kUpPix];
+        float wx[kUpPix];
 #pragma unroll
-      for (int e = 0; e < V; ++e) {
-        float r = to_f(a.e[e]) * tp.w00 + to_f(b.e[e]) * tp.w01 + to_f(c.e[e]) * tp.w10 +
-                  to_f(d.e[e]) * tp.w11;
-        if (lat) r += to_f(l.e[e]);
-        o.e[e] = from_f<T>(r);
+        for (int k = 0; k < kUpPix; ++k) {
+          const int x = min(xb + k, W - 1);  // clamped duplicates are not stored
+          const float sx = src_coord(x, Wc, W, sx_scale, ac);
+          const int x0 = static_cast<int>(sx);
+          const int x1 = min(x0 + 1, Wc - 1);
+          wx[k] = sx - static_cast<float>(x0);
+          a[k].u = __ldg(reinterpret_cast<const uint4*>(c0 + static_cast<size_t>(x0) * C + e0));
+          b[k].u = __ldg(reinterpret_cast<const uint4*>(c0 + static_cast<size_t>(x1) * C + e0));
+          c[k].u = __ldg(reinterpret_cast<const uint4*>(c1 + static_cast<size_t>(x0) * C + e0));
+          d[k].u = __ldg(reinterpret_cast<const uint4*>(c1 + static_cast<size_t>(x1) * C + e0));
+          if (lrow) l[k].u = *reinterpret_cast<const uint4*>(lrow + static_cast<size_t>(x) * C + e0);
+        }
+#pragma unroll
+        for (int k = 0; k < kUpPix; ++k) {
+          if (xb + k >= W) break;
+          const float w00 = (1.f - wy) * (1.f - wx[k]), w01 = (1.f - wy) * wx[k];
+          const float w10 = wy * (1.f - wx[k]), w11 = wy * wx[k];
+          Vec16<T> o;
+#pragma unroll
+          for (int e = 0; e < V; ++e) {
+            float v = lrow ? to_f(l[k].e[e]) : 0.f;
+            v = fmaf(to_f(a[k].e[e]), w00, v);
+            v = fmaf(to_f(b[k].e[e]), w01, v);
+            v = fmaf(to_f(c[k].e[e]), w10, v);
+            v = fmaf(to_f(d[k].e[e]), w11, v);
+            o.e[e] = from_f<T>(v);
+          }
+          *reinterpret_cast<uint4*>(orow + static_cast<size_t>(xb + k) * C + e0) = o.u;
+        }
+      } else {
+        for (int k = 0; k < kUpPix && xb + k < W; ++k) {
+          const int x = xb + k;
+          const float sx = src_coord(x, Wc, W, sx_scale, ac);
+          const int x0 = static_cast<int>(sx);
+          const int x1 = min(x0 + 1, Wc - 1);
+          const float wx = sx - static_cast<float>(x0);
+          float v = lrow ? to_f(lrow[static_cast<size_t>(x) * C + e0]) : 0.f;
+          v = fmaf(to_f(c0[static_cast<size_t>(x0) * C + e0]), (1.f - wy) * (1.f - wx), v);
+          v = fmaf(to_f(c0[static_cast<size_t>(x1) * C + e0]), (1.f - wy) * wx, v);
+          v = fmaf(to_f(c1[static_cast<size_t>(x0) * C + e0]), wy * (1.f - wx), v);
+          v = fmaf(to_f(c1[static_cast<size_t>(x1) * C + e0]), wy * wx, v);
+          orow[static_cast<size_t>(x) * C + e0] = from_f<T>(v);
+        }
       }
-      *reinterpret_cast<uint4*>(out + io) = o.u;
-    } else {
-      float r = to_f(coarse[i00]) * tp.w00 + to_f(coarse[i01]) * tp.w01 +
-                to_f(coarse[i10]) * tp.w10 + to_f(coarse[i11]) * tp.w11;
-      if (lat) r += to_f(lat[io]);
-      out[io] = from_f<T>(r);
     }
+  }
+}
+
+// Fast path for 512-byte pixels (256 channels of a 16-bit type -- every FPN map): one
+// warp per output pixel, lane = 16 bytes (8 channels), a block = 8 consecutive pixels of
+// one row, no loops; all five loads of a lane are independent and issued back to back.
+// `out` may alias `lat` (each lane reads its lateral vector before writing it).
+template <typename T>
+__global__ void __launch_bounds__(256) upsample_add_px512_kernel(
+    const T* __restrict__ coarse, const T* lat, T* out, int N, int Hc, int Wc, int H, int W,
+    int chunks, float sy_scale, float sx_scale, int ac) {
+  static_assert(sizeof(T) == 2, "16-bit types");
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (long long u = blockIdx.x; u < static_cast<long long>(N) * H * chunks; u += gridDim.x) {
+    const int r = static_cast<int>(u / chunks);
+    const int x = static_cast<int>(u - static_cast<long long>(r) * chunks) * 8 + warp;
+    if (x >= W) continue;
+    const int n = r / H;
+    const int y = r - n * H;
+    const float sy = src_coord(y, Hc, H, sy_scale, ac);
+    const float sx = src_coord(x, Wc, W, sx_scale, ac);
+    const int y0 = static_cast<int>(sy), x0 = static_cast<int>(sx);
+    const int y1 = min(y0 + 1, Hc - 1), x1 = min(x0 + 1, Wc - 1);
+    const float wy = sy - static_cast<float>(y0), wx = sx - static_cast<float>(x0);
+    const size_t io = (static_cast<size_t>(r) * W + x) * 256 + lane * 8;
+    const T* cb = coarse + static_cast<size_t>(n) * Hc * Wc * 256 + lane * 8;
+    Vec16<T> l, a, b, c, d;
+    if (lat) l.u = *reinterpret_cast<const uint4*>(lat + io);
+    a.u = __ldg(reinterpret_cast<const uint4*>(cb + (static_cast<size_t>(y0) * Wc + x0) * 256));
+    b.u = __ldg(reinterpret_cast<const uint4*>(cb + (static_cast<size_t>(y0) * Wc + x1) * 256));
+    c.u = __ldg(reinterpret_cast<const uint4*>(cb + (static_cast<size_t>(y1) * Wc + x0) * 256));
+    d.u = __ldg(reinterpret_cast<const uint4*>(cb + (static_cast<size_t>(y1) * Wc + x1) * 256));
+    const float w00 = (1.f - wy) * (1.f - wx), w01 = (1.f - wy) * wx;
+    const float w10 = wy * (1.f - wx), w11 = wy * wx;
+    Vec16<T> o;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float v = lat ? to_f(l.e[e]) : 0.f;
+      v = fmaf(to_f(a.e[e]), w00, v);
+      v = fmaf(to_f(b.e[e]), w01, v);
+      v = fmaf(to_f(c.e[e]), w10, v);
+      v = fmaf(to_f(d.e[e]), w11, v);
+      o.e[e] = from_f<T>(v);
+    }
+    *reinterpret_cast<uint4*>(out + io) = o.u;
   }
 }
 
@@ -160,23 +243,27 @@ template <typename T, bool kVec>
 __global__ void __launch_bounds__(256) p6_nhwc_kernel(const T* __restrict__ in,
                                                       T* __restrict__ out, int N, int C, int H,
                                                       int W, int H6, int W6) {
+  // Same walk as the NHWC upsample: blocks over output rows, warps over pixels,
+  // lanes over 16-byte channel vectors (coalesced 512-byte rows), 32-bit indices.
   constexpr int V = kVec ? Vec16<T>::kN : 1;
-  const int cv_per_pix = C / V;
-  const long long total = static_cast<long long>(N) * H6 * W6 * cv_per_pix;
-  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int cv = static_cast<int>(i % cv_per_pix);
-    const long long pix = i / cv_per_pix;
-    const int x = static_cast<int>(pix % W6);
-    const long long t = pix / W6;
-    const int y = static_cast<int>(t % H6);
-    const int n = static_cast<int>(t / H6);
-    const size_t src = ((static_cast<size_t>(n) * H + 2 * y) * W + 2 * x) * C + cv * V;
-    const size_t dst = static_cast<size_t>(pix) * C + cv * V;
-    if constexpr (kVec) {
-      *reinterpret_cast<uint4*>(out + dst) = __ldg(reinterpret_cast<const uint4*>(in + src));
-    } else {
-      out[dst] = in[src];
+  const int cvs = C / V;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rows = N * H6;
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    const int n = r / H6;
+    const int y = r - n * H6;
+    const T* src_row = in + (static_cast<size_t>(n) * H + 2 * y) * W * C;
+    T* dst_row = out + static_cast<size_t>(r) * W6 * C;
+    for (int x = warp; x < W6; x += 8) {
+      const T* s = src_row + static_cast<size_t>(2 * x) * C;
+      T* d = dst_row + static_cast<size_t>(x) * C;
+      for (int cv = lane; cv < cvs; cv += 32) {
+        if constexpr (kVec) {
+          *reinterpret_cast<uint4*>(d + cv * V) = __ldg(reinterpret_cast<const uint4*>(s + cv * V));
+        } else {
+          d[cv] = s[cv];
+        }
+      }
     }
   }
 }
@@ -368,13 +455,25 @@ cudaError_t upsample_add_t(const void* coarse, const void* lat, void* out, int N
     constexpr int V = Vec16<T>::kN;
     const bool vec = (C % V == 0) && aligned16(coarse) && aligned16(out) &&
                      (lat == nullptr || aligned16(lat));
-    const long long work = static_cast<long long>(N) * H * W * (vec ? C / V : C);
+    if constexpr (sizeof(T) == 2) {
+      if (vec && C == 256) {
+        const int chunks = (W + 7) / 8;
+        const long long blocks = static_cast<long long>(N) * H * chunks;
+        const int grid = blocks < (1LL << 30) ? static_cast<int>(blocks) : (1 << 30);
+        upsample_add_px512_kernel<T>
+            <<<grid, 256, 0, s>>>(c, l, o, N, Hc, Wc, H, W, chunks, sy, sx, ac);
+        return cudaGetLastError();
+      }
+    }
+    const long long units =
+        static_cast<long long>(N) * H * ((W + 8 * kUpPix - 1) / (8 * kUpPix));  // per block
+    const int grid = units < 148 * 64 ? static_cast<int>(units) : 148 * 64;
     if (vec)
       upsample_add_nhwc_kernel<T, true>
-          <<<grid_for(work, 256), 256, 0, s>>>(c, l, o, N, C, Hc, Wc, H, W, sy, sx, ac);
+          <<<grid, 256, 0, s>>>(c, l, o, N, C, Hc, Wc, H, W, sy, sx, ac);
     else
       upsample_add_nhwc_kernel<T, false>
-          <<<grid_for(work, 256), 256, 0, s>>>(c, l, o, N, C, Hc, Wc, H, W, sy, sx, ac);
+          <<<grid, 256, 0, s>>>(c, l, o, N, C, Hc, Wc, H, W, sy, sx, ac);
   } else {
     const long long work = static_cast<long long>(N) * C * H * W;
     upsample_add_nchw_kernel<T>
@@ -392,11 +491,12 @@ cudaError_t p6_t(const void* in, void* out, int N, int C, int H, int W, Layout l
   if (layout == Layout::NHWC) {
     constexpr int V = Vec16<T>::kN;
     const bool vec = (C % V == 0) && aligned16(in) && aligned16(out);
-    const long long work = static_cast<long long>(N) * H6 * W6 * (vec ? C / V : C);
+    const int rows = N * H6;
+    const int grid = rows < 148 * 8 ? rows : 148 * 8;
     if (vec)
-      p6_nhwc_kernel<T, true><<<grid_for(work, 256), 256, 0, s>>>(i, o, N, C, H, W, H6, W6);
+      p6_nhwc_kernel<T, true><<<grid, 256, 0, s>>>(i, o, N, C, H, W, H6, W6);
     else
-      p6_nhwc_kernel<T, false><<<grid_for(work, 256), 256, 0, s>>>(i, o, N, C, H, W, H6, W6);
+      p6_nhwc_kernel<T, false><<<grid, 256, 0, s>>>(i, o, N, C, H, W, H6, W6);
   } else {
     const long long work = static_cast<long long>(N) * C * H6 * W6;
     p6_nchw_kernel<T><<<grid_for(work, 256), 256, 0, s>>>(i, o, N, C, H, W, H6, W6);

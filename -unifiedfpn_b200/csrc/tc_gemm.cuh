@@ -5,7 +5,7 @@
 //     Reference semantics: lib/kernels/compute/fpn_compute_kernels.cu:127-230
 //     (1x1 conv, out = sum_c in * W[o,c] + bias[o]) followed by the top-down
 //     upsample + add of lib/core/fpn_engine.cu:274-313 (bilinear, half-pixel,
-//     scale = in/out), fused into the epilogue.
+//     scale = in/out), fused into the same accumulator.
 //
 //   Conv3x3 (mode 1): P_l[p, o] = sum_{tap, c} M_l[p + tap, c] * W3[o, tap, c] + b[o]
 //     K = 9 * 256.  The top level also emits P6 = max_pool2d(P5, k=1, s=2) = P5[::2, ::2].
@@ -17,15 +17,21 @@
 // ragged right/bottom tiles of both modes).  B (weights, [256][K] K-major) arrives
 // as a 2-D box (64, 256).  Operands use the 128-byte swizzle.
 //
+// The top-down add is itself a small GEMM on the same accumulator: over one tile,
+// bilinear(M_{l+1}) = Wb (128 px x k coarse px, 4 non-zeros per row) . Mbox (k coarse
+// px x 256 ch).  Mbox is the tile's coarse box (at most 64 pixels), fetched by TMA
+// into a B stage where, channel-contiguous, it is an MN-major B operand; Wb is written
+// into the A stage by the producer warp.  One extra k-block of 4 MMAs replaces all of
+// the epilogue's bilinear arithmetic.  (If the box cannot hold a tile's taps, the
+// epilogue reads the taps from global memory instead.)
+//
 // The fp32 accumulator lives in TMEM (two 256-column buffers, so the epilogue of
 // tile i overlaps the main loop of tile i+1).  The epilogue reads TMEM, adds the
-// bias (and, for the lateral, the bilinear sample of the coarser merged map,
-// staged per tile in shared memory by TMA), converts, writes a 128-byte
-// swizzled staging tile and stores it with a TMA tensor store (which also clips
-// ragged tiles).
+// bias, converts, writes a 128-byte swizzled staging tile and stores it with a TMA
+// tensor store (which also clips ragged tiles).
 //
 // One CTA per SM (persistent, static round-robin over tiles):
-//   warp 0      : TMA producer (one lane)
+//   warp 0      : TMA producer (lane 0 issues; the whole warp builds Wb)
 //   warp 1      : TMEM allocator + tcgen05.mma issuer (one lane)
 //   warps 2..9  : epilogue; warp w may access TMEM lanes 32*(w%4)..+31, and
 //                 handles 128 of the 256 output channels ((w-2)/4 selects which)
@@ -44,24 +50,21 @@ constexpr int kTcAStage = kTcBlockM * 128;
 constexpr int kTcBStage = kTcBlockN * 128;
 constexpr int kTcTmemCols = 2 * kTcBlockN;
 constexpr int kTcStagingPerWarp = 32 * 128;  // 32 rows x 64 channels (bf16/fp16)
-constexpr int kTcCoarseMaxPix = 80;          // coarse pixels per staged 64-channel block
+constexpr int kTcCoarseMaxPix = 64;          // coarse-box pixels = one MMA k-block
+constexpr int kTcStages = 4;
 
-template <int kMode>
 struct TcCfg {
-  static constexpr int kStages = kMode == 0 ? 3 : 4;
-  static constexpr int kCoarseBlk = kMode == 0 ? kTcCoarseMaxPix * 128 : 0;  // 1024-aligned
+  static constexpr int kStages = kTcStages;
   static constexpr int kOffB = kStages * kTcAStage;
   static constexpr int kOffStaging = kOffB + kStages * kTcBStage;
-  static constexpr int kOffCoarse = kOffStaging + kTcEpiWarps * kTcStagingPerWarp;
-  static constexpr int kOffBars = kOffCoarse + 4 * kCoarseBlk;
+  static constexpr int kOffBars = kOffStaging + kTcEpiWarps * kTcStagingPerWarp;
   static constexpr int kSmemBytes = kOffBars + 256 + 1024 /*alignment slack*/;
 };
-static_assert(TcCfg<0>::kSmemBytes <= 232448, "lateral smem");
-static_assert(TcCfg<1>::kSmemBytes <= 232448, "conv smem");
+static_assert(TcCfg::kSmemBytes <= 232448, "tc smem");
 
 struct TcGemmArgs {
   int num_tiles;
-  int num_kb;      // taps * cin_blocks
+  int num_kb;      // taps * cin_blocks (main loop only)
   int cin_blocks;  // ceil(Cin / 64)
   int N_img, H, W;
   int tile_w, tile_h, tiles_x, tiles_y;
@@ -70,7 +73,7 @@ struct TcGemmArgs {
   const void* coarse;  // null = no top-down add
   int Hc, Wc;
   float scale_y, scale_x;  // Hc / H, Wc / W
-  int cbox_w, cbox_h;      // staged coarse box (0 = read the coarse map from global memory)
+  int cbox_w, cbox_h;      // coarse box of the MMA path (0 = taps from global memory)
   // conv3x3 top level: P6 NHWC [N][H6][W6][256], or null
   void* p6;
   int H6, W6;
@@ -90,6 +93,10 @@ struct Pack<__nv_bfloat16> {
     __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&u);
     return __bfloat1622float2(v);
   }
+  __device__ static __forceinline__ uint16_t bits(float a) {
+    __nv_bfloat16 v = __float2bfloat16_rn(a);
+    return *reinterpret_cast<uint16_t*>(&v);
+  }
 };
 template <>
 struct Pack<__half> {
@@ -101,6 +108,10 @@ struct Pack<__half> {
   __device__ static __forceinline__ float2 unpack(uint32_t u) {
     __half2 v = *reinterpret_cast<__half2*>(&u);
     return __half22float2(v);
+  }
+  __device__ static __forceinline__ uint16_t bits(float a) {
+    __half v = __float2half_rn(a);
+    return *reinterpret_cast<uint16_t*>(&v);
   }
 };
 
@@ -114,8 +125,9 @@ __device__ __forceinline__ void tc_tile_origin(const TcGemmArgs& a, int tile, in
   y0 = ty * a.tile_h;
 }
 
-// Bilinear source index along one axis (half-pixel, clamped), identical on the
-// producer side (coarse box origin) and in the epilogue.
+// Bilinear source index along one axis (half-pixel, clamped).  Every step is an
+// explicitly rounded fp32 operation so the host can replay it bit for bit when it
+// sizes the coarse box.
 __device__ __forceinline__ float tc_src(int o, float scale, int in) {
   const float s = __fsub_rn(__fmul_rn(__fadd_rn(static_cast<float>(o), 0.5f), scale), 0.5f);
   return fminf(fmaxf(s, 0.f), static_cast<float>(in - 1));
@@ -126,6 +138,9 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
                "r"(v.z), "r"(v.w)
                : "memory");
 }
+__device__ __forceinline__ void st_shared_u16(uint32_t addr, uint16_t v) {
+  asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"(v) : "memory");
+}
 __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
@@ -134,35 +149,242 @@ __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
   return v;
 }
 
+// Geometry of one bilinear tap set (shared by the Wb builder and the epilogue fallback).
+struct TcTaps {
+  int ya, yb, xa, xb;
+  float w00, w01, w10, w11;
+};
+__device__ __forceinline__ TcTaps tc_taps(int py, int px, int H, int W, int Hc, int Wc,
+                                          float scale_y, float scale_x) {
+  const float sy = tc_src(min(py, H - 1), scale_y, Hc);
+  const float sx = tc_src(min(px, W - 1), scale_x, Wc);
+  TcTaps t;
+  t.ya = static_cast<int>(sy);
+  t.xa = static_cast<int>(sx);
+  t.yb = min(t.ya + 1, Hc - 1);
+  t.xb = min(t.xa + 1, Wc - 1);
+  const float wy = sy - static_cast<float>(t.ya);
+  const float wx = sx - static_cast<float>(t.xa);
+  t.w00 = (1.f - wy) * (1.f - wx);
+  t.w01 = (1.f - wy) * wx;
+  t.w10 = wy * (1.f - wx);
+  t.w11 = wy * wx;
+  return t;
+}
+
+// Whole-warp builder of the bilinear operands of one tile, written with generic
+// stores (the caller fences the async proxy afterwards):
+//   a_stage: Wb, 128 rows (tile pixels) x 64 k (box pixels), K-major 128-byte swizzle;
+//   b_stage: zeroes the box rows k >= cbox_w * cbox_h of the 4 MN-major 64-channel
+//            blocks (TMA fills rows below that) so no stale bits meet a zero weight.
+template <typename T>
+__device__ __forceinline__ void tc_build_bilinear(uint8_t* a_stage, uint8_t* b_stage, int lane,
+                                                  int x0, int y0, int tile_w, int H, int W,
+                                                  int Hc, int Wc, float scale_y, float scale_x,
+                                                  int cbox_w, int cbox_h) {
+  const uint32_t a_addr = smem_u32(a_stage);
+  const uint32_t b_addr = smem_u32(b_stage);
+  const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+  for (int i = lane; i < kTcAStage / 16; i += 32) st_shared_v4(a_addr + i * 16, z);
+  const int kbox = cbox_w * cbox_h;
+  for (int i = lane; i < 4 * (kTcCoarseMaxPix - kbox) * 8; i += 32) {
+    const int blk = i / ((kTcCoarseMaxPix - kbox) * 8);
+    const int rem = i - blk * ((kTcCoarseMaxPix - kbox) * 8);
+    const int row = kbox + (rem >> 3);
+    st_shared_v4(b_addr + blk * (kTcCoarseMaxPix * 128) + row * 128 + (rem & 7) * 16, z);
+  }
+  __syncwarp();
+  const int cy0 = static_cast<int>(tc_src(y0, scale_y, Hc));
+  const int cx0 = static_cast<int>(tc_src(x0, scale_x, Wc));
+#pragma unroll 1
+  for (int r = lane; r < kTcBlockM; r += 32) {
+    const TcTaps t = tc_taps(y0 + r / tile_w, x0 + r % tile_w, H, W, Hc, Wc, scale_y, scale_x);
+    int k[4] = {(t.ya - cy0) * cbox_w + (t.xa - cx0), (t.ya - cy0) * cbox_w + (t.xb - cx0),
+                (t.yb - cy0) * cbox_w + (t.xa - cx0), (t.yb - cy0) * cbox_w + (t.xb - cx0)};
+    float w[4] = {t.w00, t.w01, t.w10, t.w11};
+    // Corners that coincide (clamped at the map border) add their weights.
+#pragma unroll
+    for (int i = 1; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < i; ++j)
+        if (k[i] == k[j] && w[j] != 0.f) {
+          w[j] += w[i];
+          w[i] = 0.f;
+        }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (w[i] == 0.f || k[i] < 0 || k[i] >= kbox) continue;
+      const uint32_t byte = static_cast<uint32_t>(k[i]) * 2u;
+      const uint32_t off = r * 128 + ((((byte >> 4) ^ (r & 7)) & 7) << 4) + (byte & 15);
+      st_shared_u16(a_addr + off, Pack<T>::bits(w[i]));
+    }
+  }
+}
+
+// Epilogue role (warps 2..9) of the tensor-core kernels: per tile, TMEM -> registers,
+// + bias (+ global-memory bilinear taps on the lateral fallback path), convert,
+// 128-byte-swizzled staging tile, TMA tensor store; P6 rows for the top 3x3.
+template <int kMode, typename T>
+__device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtensorMap* map_out,
+                                            uint32_t tmem_base, uint64_t* accf_bar,
+                                            uint64_t* acce_bar, uint8_t* smem_stage,
+                                            volatile int* abort_flag, int warp, int lane,
+                                            bool bil_mma) {
+  const int ew = warp - 2;
+  const int quarter = warp & 3;  // TMEM lanes 32*quarter..+31
+  const int chalf = ew >> 2;     // output channels chalf*128 .. +127
+  const int row = quarter * 32 + lane;
+  const int tw = args.tile_w;
+  const uint32_t stage_addr = smem_u32(smem_stage + ew * kTcStagingPerWarp);
+  const bool taps_global = (kMode == 0) && args.coarse != nullptr && !bil_mma;
+  int acc = 0;
+  uint32_t acc_phase = 0;
+  for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x) {
+    const bool ok =
+        mbar_wait(&accf_bar[acc], acc_phase, abort_flag, args.status, kDevTimeoutEpilogue);
+    if (!__all_sync(0xffffffffu, ok)) break;
+    tc_fence_after();
+
+    int n, x0, y0;
+    tc_tile_origin(args, tile, n, x0, y0);
+    const int py = y0 + row / tw;
+    const int px = x0 + row % tw;
+    const bool valid = (py < args.H) && (px < args.W);
+
+    // Fallback only: bilinear taps of the coarser merged map from global memory.
+    TcTaps tp{};
+    const uint8_t* g00 = nullptr;
+    const uint8_t* g01 = nullptr;
+    const uint8_t* g10 = nullptr;
+    const uint8_t* g11 = nullptr;
+    if (taps_global) {
+      tp = tc_taps(py, px, args.H, args.W, args.Hc, args.Wc, args.scale_y, args.scale_x);
+      const size_t rowb = static_cast<size_t>(kTcBlockN) * sizeof(T);
+      const uint8_t* cbase = static_cast<const uint8_t*>(args.coarse) +
+                             static_cast<size_t>(n) * args.Hc * args.Wc * rowb;
+      g00 = cbase + (static_cast<size_t>(tp.ya) * args.Wc + tp.xa) * rowb;
+      g01 = cbase + (static_cast<size_t>(tp.ya) * args.Wc + tp.xb) * rowb;
+      g10 = cbase + (static_cast<size_t>(tp.yb) * args.Wc + tp.xa) * rowb;
+      g11 = cbase + (static_cast<size_t>(tp.yb) * args.Wc + tp.xb) * rowb;
+    }
+    const bool emit_p6 =
+        (kMode == 1) && (args.p6 != nullptr) && valid && ((py & 1) == 0) && ((px & 1) == 0);
+    uint8_t* p6_row = nullptr;
+    if (emit_p6) {
+      const size_t p6pix =
+          (static_cast<size_t>(n) * args.H6 + (py >> 1)) * args.W6 + (px >> 1);
+      p6_row = static_cast<uint8_t*>(args.p6) + p6pix * kTcBlockN * sizeof(T);
+    }
+    // Output box of this warp's 32 rows.
+    const int wrow0 = quarter * 32;
+    const int ox = x0 + (wrow0 % tw);
+    const int oy = y0 + wrow0 / tw;
+
+#pragma unroll 1
+    for (int step = 0; step < 2; ++step) {
+      const int col0 = chalf * 128 + step * 64;
+      uint32_t r[64];
+      __syncwarp();
+      const uint32_t taddr = tmem_base + static_cast<uint32_t>(acc * kTcBlockN + col0) +
+                             (static_cast<uint32_t>(quarter * 32) << 16);
+      tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+      tmem_ld32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+      tmem_wait_ld();
+      if (step == 1) {
+        // All of this tile's accumulator columns for this warp are in registers:
+        // hand the TMEM buffer back to the MMA warp before the memory work.
+        tc_fence_before();
+        mbar_arrive(&acce_bar[acc]);
+      }
+      float v[64];
+      const float4* b4 = reinterpret_cast<const float4*>(args.bias + col0);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float4 bb = __ldg(b4 + i);
+        v[4 * i + 0] = __uint_as_float(r[4 * i + 0]) + bb.x;
+        v[4 * i + 1] = __uint_as_float(r[4 * i + 1]) + bb.y;
+        v[4 * i + 2] = __uint_as_float(r[4 * i + 2]) + bb.z;
+        v[4 * i + 3] = __uint_as_float(r[4 * i + 3]) + bb.w;
+      }
+      if (taps_global) {
+        const size_t off = static_cast<size_t>(col0) * sizeof(T);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint4 a = __ldg(reinterpret_cast<const uint4*>(g00 + off) + j);
+          const uint4 b = __ldg(reinterpret_cast<const uint4*>(g01 + off) + j);
+          const uint4 c = __ldg(reinterpret_cast<const uint4*>(g10 + off) + j);
+          const uint4 d = __ldg(reinterpret_cast<const uint4*>(g11 + off) + j);
+          const uint32_t au[4] = {a.x, a.y, a.z, a.w};
+          const uint32_t bu[4] = {b.x, b.y, b.z, b.w};
+          const uint32_t cu[4] = {c.x, c.y, c.z, c.w};
+          const uint32_t du[4] = {d.x, d.y, d.z, d.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 fa = Pack<T>::unpack(au[e]);
+            const float2 fb = Pack<T>::unpack(bu[e]);
+            const float2 fc = Pack<T>::unpack(cu[e]);
+            const float2 fd = Pack<T>::unpack(du[e]);
+            v[8 * j + 2 * e + 0] += tp.w00 * fa.x + tp.w01 * fb.x + tp.w10 * fc.x + tp.w11 * fd.x;
+            v[8 * j + 2 * e + 1] += tp.w00 * fa.y + tp.w01 * fb.y + tp.w10 * fc.y + tp.w11 * fd.y;
+          }
+        }
+      }
+      // The previous TMA store from this warp's staging buffer must have read it.
+      if (lane == 0) bulk_wait_group_read<0>();
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        uint4 o;
+        o.x = Pack<T>::pack(v[8 * j + 0], v[8 * j + 1]);
+        o.y = Pack<T>::pack(v[8 * j + 2], v[8 * j + 3]);
+        o.z = Pack<T>::pack(v[8 * j + 4], v[8 * j + 5]);
+        o.w = Pack<T>::pack(v[8 * j + 6], v[8 * j + 7]);
+        st_shared_v4(stage_addr + lane * 128 + ((j ^ (lane & 7)) << 4), o);
+        if (emit_p6)
+          reinterpret_cast<uint4*>(p6_row + static_cast<size_t>(col0) * sizeof(T))[j] = o;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_4d(map_out, smem_stage + ew * kTcStagingPerWarp, col0, ox, oy, n);
+        bulk_commit_group();
+      }
+    }
+    if (++acc == 2) {
+      acc = 0;
+      acc_phase ^= 1u;
+    }
+  }
+  if (lane == 0) bulk_wait_group<0>();
+  __syncwarp();
+}
+
 template <int kMode, typename T>
 __global__ void __launch_bounds__(kTcThreads, 1)
     fpn_tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
                        const __grid_constant__ CUtensorMap map_b,
                        const __grid_constant__ CUtensorMap map_out,
                        const __grid_constant__ CUtensorMap map_coarse, const TcGemmArgs args) {
-  using Cfg = TcCfg<kMode>;
-  constexpr int S = Cfg::kStages;
+  constexpr int S = TcCfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint8_t* smem_a = smem;
-  uint8_t* smem_b = smem + Cfg::kOffB;
-  uint8_t* smem_stage = smem + Cfg::kOffStaging;
-  uint8_t* smem_coarse = smem + Cfg::kOffCoarse;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBars);
+  uint8_t* smem_b = smem + TcCfg::kOffB;
+  uint8_t* smem_stage = smem + TcCfg::kOffStaging;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TcCfg::kOffBars);
   uint64_t* full_bar = bars;
   uint64_t* empty_bar = bars + S;
   uint64_t* accf_bar = bars + 2 * S;
   uint64_t* acce_bar = accf_bar + 2;
   uint64_t* done_bar = acce_bar + 2;
-  uint64_t* cfull_bar = done_bar + 1;
-  uint64_t* cempty_bar = cfull_bar + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(cempty_bar + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const bool coarse_smem = (kMode == 0) && args.coarse != nullptr && args.cbox_w > 0;
+  // Top-down add through the tensor core (coarse box fits one k-block).
+  const bool bil_mma = (kMode == 0) && args.coarse != nullptr && args.cbox_w > 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -174,14 +396,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&acce_bar[b], kTcEpiWarps * 32);
     }
     mbar_init(done_bar, 1);
-    mbar_init(cfull_bar, 1);
-    mbar_init(cempty_bar, kTcEpiWarps * 32);
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tmap(&map_a);
     prefetch_tmap(&map_b);
     prefetch_tmap(&map_out);
-    if (coarse_smem) prefetch_tmap(&map_coarse);
+    if (bil_mma) prefetch_tmap(&map_coarse);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTcTmemCols);
@@ -193,60 +413,66 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      uint32_t cphase = 0;
-      int issued = 0;
-      bool ok = true;
-      const uint32_t coarse_bytes = static_cast<uint32_t>(args.cbox_w * args.cbox_h * 128 * 4);
-      for (int tile = blockIdx.x; ok && tile < args.num_tiles; tile += gridDim.x) {
-        int n, x0, y0;
-        tc_tile_origin(args, tile, n, x0, y0);
-        for (int kb = 0; kb < args.num_kb; ++kb) {
-          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, args.status,
-                         kDevTimeoutProducer)) {
-            ok = false;
-            break;
+    // ------------------------------------------------------------ TMA producer (whole warp)
+    int stage = 0;
+    uint32_t phase = 0;
+    int issued = 0;
+    bool ok = true;
+    const uint32_t coarse_bytes = static_cast<uint32_t>(args.cbox_w * args.cbox_h * 128 * 4);
+    for (int tile = blockIdx.x; ok && tile < args.num_tiles; tile += gridDim.x) {
+      int n, x0, y0;
+      tc_tile_origin(args, tile, n, x0, y0);
+      const int nkb = args.num_kb + (bil_mma ? 1 : 0);
+      for (int kb = 0; kb < nkb; ++kb) {
+        ok = mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, args.status,
+                       kDevTimeoutProducer);
+        if (!__all_sync(0xffffffffu, ok)) {
+          ok = false;
+          break;
+        }
+        if (kb < args.num_kb) {
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&full_bar[stage], kTcAStage + kTcBStage);
+            int dy = 0, dx = 0, cb = kb;
+            if constexpr (kMode == 1) {
+              const int tap = kb / args.cin_blocks;
+              cb = kb - tap * args.cin_blocks;
+              dy = tap / 3 - 1;
+              dx = tap % 3 - 1;
+            }
+            tma_load_4d(smem_a + stage * kTcAStage, &map_a, &full_bar[stage], cb * kTcBlockK,
+                        x0 + dx, y0 + dy, n,
+                        kMode == 0 ? kPolicyEvictFirst : kPolicyEvictLast);
+            tma_load_2d(smem_b + stage * kTcBStage, &map_b, &full_bar[stage], kb * kTcBlockK, 0,
+                        kPolicyEvictLast);
           }
-          mbar_arrive_expect_tx(&full_bar[stage], kTcAStage + kTcBStage);
-          int dy = 0, dx = 0, cb = kb;
-          if constexpr (kMode == 1) {
-            const int tap = kb / args.cin_blocks;
-            cb = kb - tap * args.cin_blocks;
-            dy = tap / 3 - 1;
-            dx = tap % 3 - 1;
-          }
-          tma_load_4d(smem_a + stage * kTcAStage, &map_a, &full_bar[stage], cb * kTcBlockK,
-                      x0 + dx, y0 + dy, n, kMode == 0 ? kPolicyEvictFirst : kPolicyEvictLast);
-          tma_load_2d(smem_b + stage * kTcBStage, &map_b, &full_bar[stage], kb * kTcBlockK, 0,
-                      kPolicyEvictLast);
-          ++issued;
-          if (++stage == S) {
-            stage = 0;
-            phase ^= 1u;
+        } else {
+          // Bilinear k-block: Wb into the A stage (generic stores, whole warp), the
+          // coarse box into the B stage (TMA), then one arrival with the TMA bytes.
+          tc_build_bilinear<T>(smem_a + stage * kTcAStage, smem_b + stage * kTcBStage, lane,
+                               x0, y0, args.tile_w, args.H, args.W, args.Hc, args.Wc,
+                               args.scale_y, args.scale_x, args.cbox_w, args.cbox_h);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            const int cy = static_cast<int>(tc_src(y0, args.scale_y, args.Hc));
+            const int cx = static_cast<int>(tc_src(x0, args.scale_x, args.Wc));
+            mbar_arrive_expect_tx(&full_bar[stage], coarse_bytes);
+            for (int b = 0; b < 4; ++b)
+              tma_load_4d(smem_b + stage * kTcBStage + b * (kTcCoarseMaxPix * 128), &map_coarse,
+                          &full_bar[stage], b * 64, cx, cy, n, kPolicyEvictLast);
           }
         }
-        if (!ok) break;
-        if (coarse_smem) {
-          // Coarse box for this tile, after its main-loop loads so those are not
-          // held up by the previous tile's epilogue still reading the buffer.
-          if (!mbar_wait(cempty_bar, cphase ^ 1u, abort_flag, args.status, kDevTimeoutProducer)) {
-            ok = false;
-            break;
-          }
-          const int cy = static_cast<int>(tc_src(y0, args.scale_y, args.Hc));
-          const int cx = static_cast<int>(tc_src(x0, args.scale_x, args.Wc));
-          mbar_arrive_expect_tx(cfull_bar, coarse_bytes);
-          for (int b = 0; b < 4; ++b)
-            tma_load_4d(smem_coarse + b * Cfg::kCoarseBlk, &map_coarse, cfull_bar, b * 64, cx, cy,
-                        n, kPolicyEvictLast);
-          cphase ^= 1u;
+        ++issued;
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
         }
       }
-      // Teardown: every copy this thread issued must land before the CTA exits
-      // (matters only when another role aborted early).
+    }
+    // Teardown: every copy issued must land before the CTA exits (matters only when
+    // another role aborted early).
+    if (lane == 0) {
       for (int i = 0; i < S && i < issued; ++i) {
         if (--stage < 0) {
           stage = S - 1;
@@ -254,35 +480,47 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         mbar_wait_drain(&full_bar[stage], phase);
       }
-      if (coarse_smem && issued > 0) mbar_wait_drain(cfull_bar, cphase ^ 1u);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc(kTcBlockM, kTcBlockN, Pack<T>::kFmt, Pack<T>::kFmt);
+      constexpr uint32_t idesc_bmn =
+          make_idesc(kTcBlockM, kTcBlockN, Pack<T>::kFmt, Pack<T>::kFmt, 1u);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
+      const int nkb = args.num_kb + (bil_mma ? 1 : 0);
       for (int tile = blockIdx.x; ok && tile < args.num_tiles; tile += gridDim.x) {
         if (!mbar_wait(&acce_bar[acc], acc_phase ^ 1u, abort_flag, args.status, kDevTimeoutMma))
           break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kTcBlockN);
-        for (int kb = 0; kb < args.num_kb; ++kb) {
+        for (int kb = 0; kb < nkb; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, abort_flag, args.status, kDevTimeoutMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint64_t adesc = sdesc_kmajor_sw128(smem_u32(smem_a + stage * kTcAStage));
-          const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(smem_b + stage * kTcBStage));
+          if (kb < args.num_kb) {
+            const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(smem_b + stage * kTcBStage));
 #pragma unroll
-          for (int k = 0; k < kTcBlockK / 16; ++k) {
-            // +32 bytes along K per 16-element MMA step (encoded >> 4).
-            tc_mma_f16(d_tmem, adesc + 2u * k, bdesc + 2u * k, idesc,
-                       (kb > 0 || k > 0) ? 1u : 0u);
+            for (int k = 0; k < kTcBlockK / 16; ++k) {
+              // +32 bytes along K per 16-element MMA step (encoded >> 4).
+              tc_mma_f16(d_tmem, adesc + 2u * k, bdesc + 2u * k, idesc,
+                         (kb > 0 || k > 0) ? 1u : 0u);
+            }
+          } else {
+            // Bilinear k-block: B (coarse box) is MN-major, 64-channel chunks 8 KB apart;
+            // +16 box rows (2048 bytes, encoded >> 4) per MMA step.
+            const uint64_t bdesc =
+                sdesc_mnmajor_sw128(smem_u32(smem_b + stage * kTcBStage), kTcCoarseMaxPix * 128);
+#pragma unroll
+            for (int k = 0; k < kTcBlockK / 16; ++k)
+              tc_mma_f16(d_tmem, adesc + 2u * k, bdesc + 128u * k, idesc_bmn, 1u);
           }
           tc_commit(&empty_bar[stage]);
           if (++stage == S) {
@@ -303,173 +541,228 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int ew = warp - 2;
-    const int quarter = warp & 3;  // TMEM lanes 32*quarter..+31
-    const int chalf = ew >> 2;     // output channels chalf*128 .. +127
-    const int row = quarter * 32 + lane;
-    const int tw = args.tile_w;
-    const uint32_t stage_addr = smem_u32(smem_stage + ew * kTcStagingPerWarp);
-    const uint32_t coarse_addr = smem_u32(smem_coarse);
-    int acc = 0;
-    uint32_t acc_phase = 0;
-    uint32_t cphase = 0;
-    for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x) {
-      bool ok =
-          mbar_wait(&accf_bar[acc], acc_phase, abort_flag, args.status, kDevTimeoutEpilogue);
-      if (coarse_smem && ok)
-        ok = mbar_wait(cfull_bar, cphase, abort_flag, args.status, kDevTimeoutEpilogue);
-      if (!__all_sync(0xffffffffu, ok)) break;
-      tc_fence_after();
+    tc_epilogue<kMode, T>(args, &map_out, tmem_base, accf_bar, acce_bar, smem_stage,
+                          abort_flag, warp, lane, bil_mma);
+  }
 
-      int n, x0, y0;
-      tc_tile_origin(args, tile, n, x0, y0);
-      const int py = y0 + row / tw;
-      const int px = x0 + row % tw;
-      const bool valid = (py < args.H) && (px < args.W);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTcTmemCols);
+  }
+}
 
-      // Bilinear corners in the coarser merged map (lateral mode).
-      float w00 = 0.f, w01 = 0.f, w10 = 0.f, w11 = 0.f;
-      int r00 = 0, r01 = 0, r10 = 0, r11 = 0;  // staged-box rows
-      bool corners_staged = false;
-      const uint8_t* g00 = nullptr;
-      const uint8_t* g01 = nullptr;
-      const uint8_t* g10 = nullptr;
-      const uint8_t* g11 = nullptr;
-      if (kMode == 0 && args.coarse != nullptr) {
-        const float sy = tc_src(min(py, args.H - 1), args.scale_y, args.Hc);
-        const float sx = tc_src(min(px, args.W - 1), args.scale_x, args.Wc);
-        const int ya = static_cast<int>(sy);
-        const int xa = static_cast<int>(sx);
-        const int yb = min(ya + 1, args.Hc - 1);
-        const int xb = min(xa + 1, args.Wc - 1);
-        const float wy = sy - static_cast<float>(ya);
-        const float wx = sx - static_cast<float>(xa);
-        w00 = (1.f - wy) * (1.f - wx);
-        w01 = (1.f - wy) * wx;
-        w10 = wy * (1.f - wx);
-        w11 = wy * wx;
-        if (coarse_smem) {
-          const int cy0 = static_cast<int>(tc_src(y0, args.scale_y, args.Hc));
-          const int cx0 = static_cast<int>(tc_src(x0, args.scale_x, args.Wc));
-          corners_staged = (ya - cy0) >= 0 && (yb - cy0) < args.cbox_h && (xa - cx0) >= 0 &&
-                           (xb - cx0) < args.cbox_w;
-          r00 = (ya - cy0) * args.cbox_w + (xa - cx0);
-          r01 = (ya - cy0) * args.cbox_w + (xb - cx0);
-          r10 = (yb - cy0) * args.cbox_w + (xa - cx0);
-          r11 = (yb - cy0) * args.cbox_w + (xb - cx0);
-        }
-        if (!corners_staged) {
-          const size_t rowb = static_cast<size_t>(kTcBlockN) * sizeof(T);
-          const uint8_t* cbase = static_cast<const uint8_t*>(args.coarse) +
-                                 static_cast<size_t>(n) * args.Hc * args.Wc * rowb;
-          g00 = cbase + (static_cast<size_t>(ya) * args.Wc + xa) * rowb;
-          g01 = cbase + (static_cast<size_t>(ya) * args.Wc + xb) * rowb;
-          g10 = cbase + (static_cast<size_t>(yb) * args.Wc + xa) * rowb;
-          g11 = cbase + (static_cast<size_t>(yb) * args.Wc + xb) * rowb;
-        }
-      }
-      const bool emit_p6 =
-          (kMode == 1) && (args.p6 != nullptr) && valid && ((py & 1) == 0) && ((px & 1) == 0);
-      uint8_t* p6_row = nullptr;
-      if (emit_p6) {
-        const size_t p6pix =
-            (static_cast<size_t>(n) * args.H6 + (py >> 1)) * args.W6 + (px >> 1);
-        p6_row = static_cast<uint8_t*>(args.p6) + p6pix * kTcBlockN * sizeof(T);
-      }
-      // Output box of this warp's 32 rows.
-      const int wrow0 = quarter * 32;
-      const int ox = x0 + (wrow0 % tw);
-      const int oy = y0 + wrow0 / tw;
+// ---------------------------------------------------------------------------------
+// 3x3 conv with halo reuse.  Tiles are 8 wide x 16 high.  For each 64-channel block
+// the (16+2) x (8+2) halo of the tile is fetched ONCE by TMA (zero-filled outside the
+// image = pad 1) and all nine taps read it in place: the A operand of tap (dy, dx)
+// starts at halo row dy*10 + dx, and because a tile row is exactly one 8-row swizzle
+// atom, successive atoms are a constant 10 rows (1280 bytes) apart -- a plain
+// K-major descriptor with that stride.  Per tile this moves 4 x 23 KB of activations
+// instead of 36 x 16 KB; only the weights stream per tap.
+constexpr int kHaloTileW = 8;
+constexpr int kHaloTileH = 16;
+constexpr int kHaloRows = (kHaloTileW + 2) * (kHaloTileH + 2);  // 180
+constexpr int kHaloBytes = ((kHaloRows * 128 + 1023) / 1024) * 1024;
+constexpr int kHaloStages = 4;  // weight stages
+constexpr int kHaloBufs = 2;    // halo buffers
+struct HaloCfg {
+  static constexpr int kOffHalo = kHaloStages * kTcBStage;
+  static constexpr int kOffStaging = kOffHalo + kHaloBufs * kHaloBytes;
+  static constexpr int kOffBars = kOffStaging + kTcEpiWarps * kTcStagingPerWarp;
+  static constexpr int kSmemBytes = kOffBars + 256 + 1024;
+};
+static_assert(HaloCfg::kSmemBytes <= 232448, "halo smem");
 
-#pragma unroll 1
-      for (int step = 0; step < 2; ++step) {
-        const int col0 = chalf * 128 + step * 64;
-        uint32_t r[64];
-        __syncwarp();
-        const uint32_t taddr = tmem_base + static_cast<uint32_t>(acc * kTcBlockN + col0) +
-                               (static_cast<uint32_t>(quarter * 32) << 16);
-        tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-        tmem_ld32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-        tmem_wait_ld();
-        if (step == 1) {
-          // All of this tile's accumulator columns for this warp are in registers:
-          // hand the TMEM buffer back to the MMA warp before the memory work.
-          tc_fence_before();
-          mbar_arrive(&acce_bar[acc]);
-        }
-        float v[64];
-        const float4* b4 = reinterpret_cast<const float4*>(args.bias + col0);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float4 bb = __ldg(b4 + i);
-          v[4 * i + 0] = __uint_as_float(r[4 * i + 0]) + bb.x;
-          v[4 * i + 1] = __uint_as_float(r[4 * i + 1]) + bb.y;
-          v[4 * i + 2] = __uint_as_float(r[4 * i + 2]) + bb.z;
-          v[4 * i + 3] = __uint_as_float(r[4 * i + 3]) + bb.w;
-        }
-        if (kMode == 0 && args.coarse != nullptr) {
-          const int blk = col0 >> 6;  // 64-channel block of the staged coarse box
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            uint4 a, b, c, d;
-            if (corners_staged) {
-              const uint32_t base = coarse_addr + blk * Cfg::kCoarseBlk;
-              a = ld_shared_v4(base + r00 * 128 + ((j ^ (r00 & 7)) << 4));
-              b = ld_shared_v4(base + r01 * 128 + ((j ^ (r01 & 7)) << 4));
-              c = ld_shared_v4(base + r10 * 128 + ((j ^ (r10 & 7)) << 4));
-              d = ld_shared_v4(base + r11 * 128 + ((j ^ (r11 & 7)) << 4));
-            } else {
-              const size_t off = static_cast<size_t>(col0) * sizeof(T);
-              a = __ldg(reinterpret_cast<const uint4*>(g00 + off) + j);
-              b = __ldg(reinterpret_cast<const uint4*>(g01 + off) + j);
-              c = __ldg(reinterpret_cast<const uint4*>(g10 + off) + j);
-              d = __ldg(reinterpret_cast<const uint4*>(g11 + off) + j);
+// K-major 128B-swizzle descriptor whose 8-row atoms are `atom_stride` bytes apart and
+// whose start need not be 1024-byte aligned.  The base-offset field stays 0: the
+// hardware applies the swizzle to the computed address bits, exactly as TMA did when
+// it wrote the halo (verified against the CPU oracle; encoding the start's phase in
+// the base-offset field gives wrong results).
+__device__ __forceinline__ uint64_t sdesc_kmajor_sw128_stride(uint32_t saddr,
+                                                              uint32_t atom_stride) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(1) << 16;
+  d |= static_cast<uint64_t>((atom_stride >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    fpn_conv3x3_halo_kernel(const __grid_constant__ CUtensorMap map_a,
+                            const __grid_constant__ CUtensorMap map_b,
+                            const __grid_constant__ CUtensorMap map_out, const TcGemmArgs args) {
+  constexpr int S = kHaloStages;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint8_t* smem_b = smem;
+  uint8_t* smem_halo = smem + HaloCfg::kOffHalo;
+  uint8_t* smem_stage = smem + HaloCfg::kOffStaging;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + HaloCfg::kOffBars);
+  uint64_t* full_bar = bars;
+  uint64_t* empty_bar = bars + S;
+  uint64_t* hfull_bar = bars + 2 * S;
+  uint64_t* hempty_bar = hfull_bar + kHaloBufs;
+  uint64_t* accf_bar = hempty_bar + kHaloBufs;
+  uint64_t* acce_bar = accf_bar + 2;
+  uint64_t* done_bar = acce_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int cin_blocks = args.cin_blocks;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int h = 0; h < kHaloBufs; ++h) {
+      mbar_init(&hfull_bar[h], 1);
+      mbar_init(&hempty_bar[h], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf_bar[b], 1);
+      mbar_init(&acce_bar[b], kTcEpiWarps * 32);
+    }
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&map_a);
+    prefetch_tmap(&map_b);
+    prefetch_tmap(&map_out);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTcTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0, hb = 0, issued = 0, hissued = 0;
+      uint32_t phase = 0, hphase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < args.num_tiles; tile += gridDim.x) {
+        int n, x0, y0;
+        tc_tile_origin(args, tile, n, x0, y0);
+        for (int cb = 0; ok && cb < cin_blocks; ++cb) {
+          if (!mbar_wait(&hempty_bar[hb], hphase ^ 1u, abort_flag, args.status,
+                         kDevTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&hfull_bar[hb], kHaloRows * 128);
+          tma_load_4d(smem_halo + hb * kHaloBytes, &map_a, &hfull_bar[hb], cb * kTcBlockK, x0 - 1,
+                      y0 - 1, n, kPolicyEvictLast);
+          ++hissued;
+          if (++hb == kHaloBufs) {
+            hb = 0;
+            hphase ^= 1u;
+          }
+          for (int tap = 0; tap < 9; ++tap) {
+            if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, args.status,
+                           kDevTimeoutProducer)) {
+              ok = false;
+              break;
             }
-            const uint32_t au[4] = {a.x, a.y, a.z, a.w};
-            const uint32_t bu[4] = {b.x, b.y, b.z, b.w};
-            const uint32_t cu[4] = {c.x, c.y, c.z, c.w};
-            const uint32_t du[4] = {d.x, d.y, d.z, d.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 fa = Pack<T>::unpack(au[e]);
-              const float2 fb = Pack<T>::unpack(bu[e]);
-              const float2 fc = Pack<T>::unpack(cu[e]);
-              const float2 fd = Pack<T>::unpack(du[e]);
-              v[8 * j + 2 * e + 0] += w00 * fa.x + w01 * fb.x + w10 * fc.x + w11 * fd.x;
-              v[8 * j + 2 * e + 1] += w00 * fa.y + w01 * fb.y + w10 * fc.y + w11 * fd.y;
+            mbar_arrive_expect_tx(&full_bar[stage], kTcBStage);
+            tma_load_2d(smem_b + stage * kTcBStage, &map_b, &full_bar[stage],
+                        tap * (cin_blocks * kTcBlockK) + cb * kTcBlockK, 0, kPolicyEvictLast);
+            ++issued;
+            if (++stage == S) {
+              stage = 0;
+              phase ^= 1u;
             }
           }
         }
-        // The previous TMA store from this warp's staging buffer must have read it.
-        if (lane == 0) bulk_wait_group_read<0>();
-        __syncwarp();
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          uint4 o;
-          o.x = Pack<T>::pack(v[8 * j + 0], v[8 * j + 1]);
-          o.y = Pack<T>::pack(v[8 * j + 2], v[8 * j + 3]);
-          o.z = Pack<T>::pack(v[8 * j + 4], v[8 * j + 5]);
-          o.w = Pack<T>::pack(v[8 * j + 6], v[8 * j + 7]);
-          st_shared_v4(stage_addr + lane * 128 + ((j ^ (lane & 7)) << 4), o);
-          if (emit_p6)
-            reinterpret_cast<uint4*>(p6_row + static_cast<size_t>(col0) * sizeof(T))[j] = o;
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_4d(&map_out, smem_stage + ew * kTcStagingPerWarp, col0, ox, oy, n);
-          bulk_commit_group();
-        }
       }
-      if (coarse_smem) mbar_arrive(cempty_bar);
-      if (coarse_smem) cphase ^= 1u;
-      if (++acc == 2) {
-        acc = 0;
-        acc_phase ^= 1u;
+      for (int i = 0; i < S && i < issued; ++i) {
+        if (--stage < 0) {
+          stage = S - 1;
+          phase ^= 1u;
+        }
+        mbar_wait_drain(&full_bar[stage], phase);
+      }
+      for (int i = 0; i < kHaloBufs && i < hissued; ++i) {
+        if (--hb < 0) {
+          hb = kHaloBufs - 1;
+          hphase ^= 1u;
+        }
+        mbar_wait_drain(&hfull_bar[hb], hphase);
       }
     }
-    if (lane == 0) bulk_wait_group<0>();
-    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc(kTcBlockM, kTcBlockN, Pack<T>::kFmt, Pack<T>::kFmt);
+      int stage = 0, hb = 0, acc = 0;
+      uint32_t phase = 0, hphase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < args.num_tiles; tile += gridDim.x) {
+        if (!mbar_wait(&acce_bar[acc], acc_phase ^ 1u, abort_flag, args.status, kDevTimeoutMma))
+          break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kTcBlockN);
+        for (int cb = 0; ok && cb < cin_blocks; ++cb) {
+          if (!mbar_wait(&hfull_bar[hb], hphase, abort_flag, args.status, kDevTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t halo_addr = smem_u32(smem_halo + hb * kHaloBytes);
+          for (int tap = 0; tap < 9; ++tap) {
+            if (!mbar_wait(&full_bar[stage], phase, abort_flag, args.status, kDevTimeoutMma)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const int dy = tap / 3, dx = tap % 3;
+            const uint64_t adesc = sdesc_kmajor_sw128_stride(
+                halo_addr + static_cast<uint32_t>((dy * (kHaloTileW + 2) + dx) * 128),
+                (kHaloTileW + 2) * 128);
+            const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(smem_b + stage * kTcBStage));
+#pragma unroll
+            for (int k = 0; k < kTcBlockK / 16; ++k)
+              tc_mma_f16(d_tmem, adesc + 2u * k, bdesc + 2u * k, idesc,
+                         (cb > 0 || tap > 0 || k > 0) ? 1u : 0u);
+            tc_commit(&empty_bar[stage]);
+            if (++stage == S) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          }
+          if (!ok) break;
+          tc_commit(&hempty_bar[hb]);
+          if (++hb == kHaloBufs) {
+            hb = 0;
+            hphase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&accf_bar[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      tc_commit(done_bar);
+      mbar_wait_drain(done_bar, 0);
+    }
+  } else {
+    tc_epilogue<1, T>(args, &map_out, tmem_base, accf_bar, acce_bar, smem_stage, abort_flag, warp,
+                      lane, false);
   }
 
   tc_fence_before();

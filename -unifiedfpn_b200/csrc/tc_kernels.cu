@@ -85,6 +85,32 @@ cudaError_t encode_weights(CUtensorMap* map, DType dt, const void* base, int K) 
   return encode(map, dt, 2, base, dims, strides, box);
 }
 
+// Host replay of the device's tc_src (every step rounded to fp32, no contraction).
+float host_src(int o, float scale, int in) {
+  volatile float a = static_cast<float>(o) + 0.5f;
+  volatile float b = a * scale;
+  volatile float c = b - 0.5f;
+  float r = c;
+  if (r < 0.f) r = 0.f;
+  const float hi = static_cast<float>(in - 1);
+  if (r > hi) r = hi;
+  return r;
+}
+
+// Largest number of coarse rows (or columns) the bilinear taps of one tile of `tile`
+// outputs can touch, over all tiles of an `out`-long axis.
+int coarse_span(int out, int tile, float scale, int in) {
+  int span = 0;
+  for (int o0 = 0; o0 < out; o0 += tile) {
+    const int lo = static_cast<int>(host_src(o0, scale, in));
+    const int last = o0 + tile - 1 < out - 1 ? o0 + tile - 1 : out - 1;
+    int hi = static_cast<int>(host_src(last, scale, in)) + 1;
+    if (hi > in - 1) hi = in - 1;
+    if (hi - lo + 1 > span) span = hi - lo + 1;
+  }
+  return span;
+}
+
 bool valid_tiling(Conv3x3Tiling t) {
   return t.tile_w >= 8 && t.tile_w <= 128 && (t.tile_w & (t.tile_w - 1)) == 0 &&
          t.tile_w * t.tile_h == kTcBlockM;
@@ -108,14 +134,33 @@ cudaError_t launch_t(const TcPlan& p, cudaStream_t s) {
   if (dev < 64 && !configured[dev]) {
     cudaError_t e = cudaFuncSetAttribute(fpn_tc_gemm_kernel<kMode, T>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         TcCfg<kMode>::kSmemBytes);
+                                         TcCfg::kSmemBytes);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
   TcGemmArgs a;
   std::memcpy(&a, p.args, sizeof(a));
-  fpn_tc_gemm_kernel<kMode, T><<<p.grid, kTcThreads, TcCfg<kMode>::kSmemBytes, s>>>(
+  fpn_tc_gemm_kernel<kMode, T><<<p.grid, kTcThreads, TcCfg::kSmemBytes, s>>>(
       p.map_a, p.map_b, p.map_out, p.map_coarse, a);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_halo_t(const TcPlan& p, cudaStream_t s) {
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(fpn_conv3x3_halo_kernel<T>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         HaloCfg::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  TcGemmArgs a;
+  std::memcpy(&a, p.args, sizeof(a));
+  fpn_conv3x3_halo_kernel<T><<<p.grid, kTcThreads, HaloCfg::kSmemBytes, s>>>(
+      p.map_a, p.map_b, p.map_out, a);
   return cudaGetLastError();
 }
 
@@ -183,11 +228,11 @@ cudaError_t plan_tc_lateral(TcPlan& plan, DType dt, const void* x, const void* w
     a.Wc = Wc;
     a.scale_y = static_cast<float>(Hc) / static_cast<float>(H);
     a.scale_x = static_cast<float>(Wc) / static_cast<float>(W);
-    // Coarse rows/cols a tile's bilinear taps can touch: the span of the source
-    // coordinates of tile_h (tile_w) consecutive outputs plus the +1 neighbour.
-    const int ch = static_cast<int>(std::ceil((tiling.tile_h - 1) * a.scale_y)) + 2;
-    const int cw = static_cast<int>(std::ceil((tiling.tile_w - 1) * a.scale_x)) + 2;
-    if (ch * cw <= kTcCoarseMaxPix && ch <= 256 && cw <= 256) {
+    // Coarse box of the tensor-core top-down add: the exact span of the taps of any
+    // tile (replaying the device arithmetic); must fit one 64-pixel k-block.
+    const int ch = coarse_span(H, tiling.tile_h, a.scale_y, Hc);
+    const int cw = coarse_span(W, tiling.tile_w, a.scale_x, Wc);
+    if (ch * cw <= kTcCoarseMaxPix) {
       a.cbox_h = ch;
       a.cbox_w = cw;
       if ((e = encode_nhwc(&plan.map_coarse, dt, coarse, N, Hc, Wc, kTcBlockN, cw, ch)) !=
@@ -226,7 +271,13 @@ cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w
   a.H6 = (H - 1) / 2 + 1;
   a.W6 = (W - 1) / 2 + 1;
   a.status = status;
-  cudaError_t e = encode_nhwc(&plan.map_a, dt, x, N, H, W, C, tiling.tile_w, tiling.tile_h);
+  const bool halo = tiling.halo;
+  if (halo && (tiling.tile_w != kHaloTileW || tiling.tile_h != kHaloTileH))
+    return cudaErrorInvalidValue;
+  // Halo path: one (tile_w + 2) x (tile_h + 2) box per channel block, origin (-1, -1).
+  cudaError_t e = halo ? encode_nhwc(&plan.map_a, dt, x, N, H, W, C, kHaloTileW + 2,
+                                     kHaloTileH + 2)
+                       : encode_nhwc(&plan.map_a, dt, x, N, H, W, C, tiling.tile_w, tiling.tile_h);
   if (e != cudaSuccess) return e;
   if ((e = encode_weights(&plan.map_b, dt, w, 9 * C)) != cudaSuccess) return e;
   const int sw = tiling.tile_w < 32 ? tiling.tile_w : 32;
@@ -234,7 +285,7 @@ cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w
     return e;
   plan.map_coarse = plan.map_out;
   std::memcpy(plan.args, &a, sizeof(a));
-  plan.mode = 1;
+  plan.mode = halo ? 2 : 1;
   plan.dtype = dt;
   plan.num_tiles = a.num_tiles;
   const int cap = max_ctas > 0 ? max_ctas : sm_count();
@@ -244,30 +295,35 @@ cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w
 
 static_assert(sizeof(NeckParams) <= sizeof(NeckPlan::params), "NeckPlan::params too small");
 
-cudaError_t plan_neck(NeckPlan& plan, DType dt, int N, const NeckLevel* lv, void* p6,
-                      int* sched, int* status, int max_ctas, unsigned long long* trace) {
+cudaError_t plan_neck_jobs(NeckPlan& plan, DType dt, int N, const NeckLevel* lv, void* p6,
+                           const NeckJobSpec* specs, int num_specs, int* sched, int* status,
+                           int max_ctas, unsigned long long* trace) {
   if (dt != DType::BF16 && dt != DType::F16) return cudaErrorInvalidValue;
-  if (N <= 0 || !sched) return cudaErrorInvalidValue;
+  if (N <= 0 || !sched || num_specs < 1 || num_specs > kNeckMaxJobs) return cudaErrorInvalidValue;
   NeckParams* P = reinterpret_cast<NeckParams*>(plan.params);
   std::memset(plan.params, 0, sizeof(plan.params));
   int lat_tiles[4] = {};
-  for (int l = 0; l < 4; ++l) {
-    const NeckLevel& L = lv[l];
-    if (!valid_tiling(L.lat_tiling) || !valid_tiling(L.conv_tiling)) return cudaErrorInvalidValue;
-    if (L.Cin <= 0 || L.Cin % 8 != 0 || L.H <= 0 || L.W <= 0) return cudaErrorInvalidValue;
-    if (!aligned16(L.merged) || !aligned16(L.out) || !aligned16(L.lat_b) || !aligned16(L.conv_b))
+  bool lat_in_launch[4] = {};
+  for (int j = 0; j < num_specs; ++j) {
+    const NeckJobSpec& s = specs[j];
+    if (s.level < 0 || s.level > 3 || (s.mode != 0 && s.mode != 1)) return cudaErrorInvalidValue;
+    if (s.mode == 0 && s.coarse && s.level == 3) return cudaErrorInvalidValue;
+    const NeckLevel& L = lv[s.level];
+    const Conv3x3Tiling t = s.mode == 0 ? L.lat_tiling : L.conv_tiling;
+    if (!valid_tiling(t)) return cudaErrorInvalidValue;
+    if (L.H <= 0 || L.W <= 0 || !aligned16(L.merged)) return cudaErrorInvalidValue;
+    if (s.mode == 0) {
+      if (L.Cin <= 0 || L.Cin % 8 != 0 || !aligned16(L.lat_b)) return cudaErrorInvalidValue;
+      if (lat_in_launch[s.level]) return cudaErrorInvalidValue;
+      lat_in_launch[s.level] = true;
+      lat_tiles[s.level] = ((L.W + t.tile_w - 1) / t.tile_w) * ((L.H + t.tile_h - 1) / t.tile_h) * N;
+    } else if (!aligned16(L.out) || !aligned16(L.conv_b)) {
       return cudaErrorMisalignedAddress;
-    lat_tiles[l] = ((L.W + L.lat_tiling.tile_w - 1) / L.lat_tiling.tile_w) *
-                   ((L.H + L.lat_tiling.tile_h - 1) / L.lat_tiling.tile_h) * N;
+    }
   }
-  // Dispatch order: each job only depends on jobs before it.  All laterals go first:
-  // their main loops depend on nothing, so every SM can work on them while the
-  // top-down chain (lat5 -> lat4 -> lat3 -> lat2 epilogues) resolves; the 3x3 tiles,
-  // the bulk of the FLOPs, follow and fill the machine.
-  const int order[8][2] = {{0, 3}, {0, 2}, {0, 1}, {0, 0}, {1, 3}, {1, 2}, {1, 1}, {1, 0}};
   int start = 0;
-  for (int j = 0; j < 8; ++j) {
-    const int mode = order[j][0], l = order[j][1];
+  for (int j = 0; j < num_specs; ++j) {
+    const int mode = specs[j].mode, l = specs[j].level;
     const NeckLevel& L = lv[l];
     NeckJob& J = P->jobs[j];
     J.mode = mode;
@@ -287,24 +343,31 @@ cudaError_t plan_neck(NeckPlan& plan, DType dt, int N, const NeckLevel* lv, void
     cudaError_t e;
     const int sw = t.tile_w < 32 ? t.tile_w : 32;
     if (mode == 0) {
+      // Publish completions only if a later job of this launch waits on this level.
+      for (int k = j + 1; k < num_specs; ++k)
+        if ((specs[k].mode == 1 && specs[k].level == l) ||
+            (specs[k].mode == 0 && specs[k].coarse && specs[k].level == l - 1))
+          J.publish = 1;
       J.cin_blocks = (L.Cin + kTcBlockK - 1) / kTcBlockK;
       J.num_kb = J.cin_blocks;
       J.bias = L.lat_b;
-      if ((e = encode_nhwc(&J.map_a, dt, L.x, N, L.H, L.W, L.Cin, t.tile_w, t.tile_h)) != cudaSuccess)
+      if ((e = encode_nhwc(&J.map_a, dt, L.x, N, L.H, L.W, L.Cin, t.tile_w, t.tile_h)) !=
+          cudaSuccess)
         return e;
       if ((e = encode_weights(&J.map_b, dt, L.lat_w, L.Cin)) != cudaSuccess) return e;
       if ((e = encode_nhwc(&J.map_out, dt, L.merged, N, L.H, L.W, kTcBlockN, sw, 32 / sw)) !=
           cudaSuccess)
         return e;
       J.map_coarse = J.map_out;
-      if (l < 3) {
+      if (specs[j].coarse) {
         const NeckLevel& C = lv[l + 1];
         J.coarse = C.merged;
         J.Hc = C.H;
         J.Wc = C.W;
         J.scale_y = static_cast<float>(C.H) / static_cast<float>(L.H);
         J.scale_x = static_cast<float>(C.W) / static_cast<float>(L.W);
-        J.dep_count = lat_tiles[l + 1];
+        // Wait for M_{l+1} only if its lateral runs in this launch (else it is complete).
+        J.dep_count = lat_in_launch[l + 1] ? lat_tiles[l + 1] : 0;
         const int ch = static_cast<int>(std::ceil((t.tile_h - 1) * J.scale_y)) + 2;
         const int cw = static_cast<int>(std::ceil((t.tile_w - 1) * J.scale_x)) + 2;
         if (ch * cw <= kTcCoarseMaxPix && ch <= 256 && cw <= 256) {
@@ -319,8 +382,10 @@ cudaError_t plan_neck(NeckPlan& plan, DType dt, int N, const NeckLevel* lv, void
       J.cin_blocks = kTcBlockN / kTcBlockK;
       J.num_kb = 9 * J.cin_blocks;
       J.bias = L.conv_b;
-      J.dep_level = l;
-      J.dep_count = lat_tiles[l];
+      if (lat_in_launch[l]) {
+        J.dep_level = l;
+        J.dep_count = lat_tiles[l];
+      }
       if ((e = encode_nhwc(&J.map_a, dt, L.merged, N, L.H, L.W, kTcBlockN, t.tile_w,
                            t.tile_h)) != cudaSuccess)
         return e;
@@ -337,7 +402,7 @@ cudaError_t plan_neck(NeckPlan& plan, DType dt, int N, const NeckLevel* lv, void
       }
     }
   }
-  P->num_jobs = 8;
+  P->num_jobs = num_specs;
   P->total_tiles = start;
   for (int l = 0; l < 4; ++l) P->lat_tiles[l] = lat_tiles[l];
   P->trace = trace;
@@ -348,6 +413,17 @@ cudaError_t plan_neck(NeckPlan& plan, DType dt, int N, const NeckLevel* lv, void
   const int cap = max_ctas > 0 ? max_ctas : sm_count();
   plan.grid = start < cap ? start : cap;
   return cudaSuccess;
+}
+
+cudaError_t plan_neck(NeckPlan& plan, DType dt, int N, const NeckLevel* lv, void* p6,
+                      int* sched, int* status, int max_ctas, unsigned long long* trace) {
+  // Dispatch order: each job only depends on jobs before it.  All laterals go first:
+  // their main loops depend on nothing, so every SM can work on them while the
+  // top-down chain (lat5 -> lat4 -> lat3 -> lat2 epilogues) resolves; the 3x3 tiles,
+  // the bulk of the FLOPs, follow and fill the machine.
+  const NeckJobSpec specs[8] = {{0, 3, 0}, {0, 2, 1}, {0, 1, 1}, {0, 0, 1},
+                                {1, 3, 0}, {1, 2, 0}, {1, 1, 0}, {1, 0, 0}};
+  return plan_neck_jobs(plan, dt, N, lv, p6, specs, 8, sched, status, max_ctas, trace);
 }
 
 namespace {
@@ -380,6 +456,10 @@ cudaError_t launch_tc(const TcPlan& plan, cudaStream_t s) {
   if (plan.mode == 0) {
     return plan.dtype == DType::BF16 ? launch_t<0, __nv_bfloat16>(plan, s)
                                      : launch_t<0, __half>(plan, s);
+  }
+  if (plan.mode == 2) {
+    return plan.dtype == DType::BF16 ? launch_halo_t<__nv_bfloat16>(plan, s)
+                                     : launch_halo_t<__half>(plan, s);
   }
   return plan.dtype == DType::BF16 ? launch_t<1, __nv_bfloat16>(plan, s)
                                    : launch_t<1, __half>(plan, s);

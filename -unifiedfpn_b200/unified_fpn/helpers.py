@@ -7,6 +7,12 @@ import torch
 
 from . import _lib
 
+# Stage names of get_performance_breakdown()'s eight kernel times.
+STAGES_TC = ["laterals_P5_P4_P3", "conv3x3_P5", "merge_P4", "conv3x3_P4", "merge_P3", "conv3x3_P3",
+             "lateral_P2_fused_add", "conv3x3_P2"]
+STAGES_FP32 = ["lateral_P5", "conv3x3_P5", "lateral_P4", "conv3x3_P4", "lateral_P3", "conv3x3_P3",
+               "lateral_P2", "conv3x3_P2"]
+
 
 def benchmark_fpn(backbone_features, num_iterations: int = 100, warmup_iterations: int = 10, fpn=None):
     """Times the neck with CUDA events (reference: python/__init__.py:82-133).
@@ -38,8 +44,7 @@ def profile_fpn(backbone_features, fpn=None):
     fpn = fpn or UnifiedFPN(device=backbone_features[0].device)
     fpn(backbone_features)  # configure + weights
     kt, mt = fpn.get_performance_breakdown(backbone_features)
-    names = ["lateral_P5", "conv3x3_P5", "lateral_P4", "conv3x3_P4",
-             "lateral_P3", "conv3x3_P3", "lateral_P2", "conv3x3_P2"]
+    names = STAGES_FP32 if backbone_features[0].dtype == torch.float32 else STAGES_TC
     return {
         "kernel_times_ms": dict(zip(names, kt.tolist())),
         "forward_time_ms": float(mt[0]),

@@ -318,9 +318,9 @@ def main():
     if not args.no_roofline:
         kt, mt = fpn.get_performance_breakdown(feats[0])  # one serialised, event-timed forward
         total = float(kt.sum().item())
-        kernel_share = {n: round(float(v) / total, 4) for n, v in zip(
-            ["lateral_P5", "conv3x3_P5", "lateral_P4", "conv3x3_P4", "lateral_P3", "conv3x3_P3",
-             "lateral_P2", "conv3x3_P2"], kt.tolist())} if total > 0 else None
+        from unified_fpn.helpers import STAGES_TC
+        kernel_share = {n: {"ms": round(float(v), 4), "share": round(float(v) / total, 4)}
+                        for n, v in zip(STAGES_TC, kt.tolist())} if total > 0 else None
         h2, w2 = sizes[0]
         x = torch.randn(B, 256, h2, w2, device=dev, generator=gen).to(dtype).contiguous(
             memory_format=torch.channels_last)

@@ -127,7 +127,9 @@ struct FPNTensor {
 };
 
 struct FPNKernelConfig {
-  int tile_size = 16;            // 3x3 conv spatial tile width (tile height = 128 / width); 0 = auto
+  // 3x3 conv: 0 = automatic (tuned tiling if any, else 8 x 16 tiles with halo reuse);
+  // 8..128 = plain tiles of that width (tile height = 128 / width).
+  int tile_size = 0;
   int channels_per_thread = 8;   // accepted for API compatibility
   int shared_mem_size = 0;       // accepted for API compatibility
   bool use_tensor_cores = true;  // false forces the fp32 CUDA-core path
@@ -156,7 +158,9 @@ struct FPNPerformanceMetrics {
   float compute_utilization;  // achieved TFLOP/s / measured-peak TFLOP/s of the last timed forward
   size_t peak_memory_usage_bytes;
   int num_kernel_launches;  // counted, not estimated
-  // Per-kernel device times of the last profiled forward:
-  // [lat P5, 3x3 P5, lat P4, 3x3 P4, lat P3, 3x3 P3, lat P2, 3x3 P2]
+  // Per-stage device times of the last profiled (serialised) forward.  Tensor-core path:
+  // [laterals P5+P4+P3 (one grouped launch), 3x3 P5 (+P6), merge P4, 3x3 P4, merge P3,
+  //  3x3 P3, lateral P2 (+fused top-down add), 3x3 P2];
+  // fp32 path: [lat P5, 3x3 P5, lat P4, 3x3 P4, lat P3, 3x3 P3, lat P2, 3x3 P2].
   float kernel_times_ms[8];
 };

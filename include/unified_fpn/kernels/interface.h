@@ -54,7 +54,18 @@ cudaError_t launch_fp32_conv3x3(const float* x, const float* w, const float* bia
 struct Conv3x3Tiling {
   int tile_w = 16;
   int tile_h = 8;
+  // 3x3 only: 8 x 16 tiles whose (18 x 10) halo is loaded once per 64-channel block
+  // and shared by the nine taps (instead of one shifted box per tap).
+  bool halo = false;
 };
+// The 3x3 default: halo reuse with 8 x 16 tiles.
+inline Conv3x3Tiling halo_tiling() {
+  Conv3x3Tiling t;
+  t.tile_w = 8;
+  t.tile_h = 16;
+  t.halo = true;
+  return t;
+}
 
 // Everything one tensor-core launch needs, built on the host once per
 // (pointers, shapes) and replayable: the TMA descriptors (A, B, output,
@@ -65,7 +76,7 @@ struct TcPlan {
   alignas(64) CUtensorMap map_out;
   alignas(64) CUtensorMap map_coarse;
   unsigned char args[256];  // TcGemmArgs, opaque outside tc_kernels.cu
-  int mode = 0;             // 0 lateral, 1 conv3x3
+  int mode = 0;             // 0 lateral, 1 conv3x3, 2 conv3x3 with halo reuse
   DType dtype = DType::BF16;
   int grid = 0;
   int num_tiles = 0;
@@ -111,6 +122,18 @@ struct NeckPlan {
 cudaError_t plan_neck(NeckPlan& plan, DType dt, int N, const NeckLevel* levels, void* p6,
                       int* sched, int* status, int max_ctas,
                       unsigned long long* trace = nullptr);
+// General form: any subset of the 8 jobs, in dispatch order (a job may only depend on
+// jobs before it).  mode 0 = lateral of `level` (coarse = 1: fused top-down add of
+// level+1's merged map), mode 1 = 3x3 of `level`.  A job waits on a level only if that
+// level's lateral runs in the same launch; otherwise its input must be complete before.
+struct NeckJobSpec {
+  int mode;
+  int level;
+  int coarse;
+};
+cudaError_t plan_neck_jobs(NeckPlan& plan, DType dt, int N, const NeckLevel* levels, void* p6,
+                           const NeckJobSpec* specs, int num_specs, int* sched, int* status,
+                           int max_ctas, unsigned long long* trace = nullptr);
 cudaError_t launch_neck(const NeckPlan& plan, cudaStream_t s);
 cudaError_t launch_tc(const TcPlan& plan, cudaStream_t s);
 

@@ -120,7 +120,8 @@ int ufpn_lateral_conv(int dtype, int layout, const void* x, const void* w, const
  * fpn_compute_kernels.cu:277-340) with the full conv of the standard neck.
  *   dtype F16/BF16: NHWC x, w in dtype packed [256][9][256] (ufpn_pack_conv3x3_weights).
  *   dtype F32: NCHW x, w fp32 [256][256][3][3].
- * tile_w: spatial tile width of the tensor-core path (8..128, 0 = heuristic). */
+ * tile_w: 0 = 8 x 16 tiles with halo reuse (default: each 64-channel halo is loaded once
+ * and shared by the nine taps); 8..128 = plain tiles of that width (one box per tap). */
 int ufpn_conv3x3(int dtype, const void* x, const void* w, const float* bias, void* out,
                  void* p6, int N, int H, int W, int tile_w, void* stream);
 

@@ -86,24 +86,44 @@ def test_neck_r50_800x1216_batch2_full_size(cuda_device):
                                   (O.SWIN_CHANNELS, [(100, 167), (50, 84), (25, 42), (13, 21)], 1),
                                   (O.R50_CHANNELS, O.level_sizes(800, 1216), 2)])
 def test_fused_neck_kernel_matches_per_level_kernels(cuda_device, geom):
-    """The single persistent neck kernel (device-side level dependencies) and the eight
-    per-level kernels compute every tile identically: outputs must be bitwise equal."""
+    """The single persistent neck kernel (device-side level dependencies) and the split
+    schedule (grouped small laterals, in-place merges, fused P2 lateral, per-level 3x3s)
+    agree within the bf16 tolerance (the split schedule rounds L4/L3 to bf16 before their
+    top-down add), and repeated fused launches are bitwise identical."""
     import unified_fpn as U
     chans, sizes, batch = geom
     feats = [_cl(f.to(torch.bfloat16).cuda()) for f in O.make_features(batch, chans, sizes, seed=33)]
     fpn = U.UnifiedFPN()
+    fpn.set_schedule(fused_neck_kernel=True)
     fused = _run(fpn, feats)
     assert fpn.device_status() == 0
     fpn.set_schedule(fused_neck_kernel=False)
     split = _run(fpn, feats)
+    assert fpn.device_status() == 0
     for a, b in zip(fused, split):
-        assert torch.equal(a, b)
+        assert O.rel_err(a.float().cpu(), b.float().cpu()) < TOL16
     fpn.set_schedule(fused_neck_kernel=True)
     for _ in range(3):  # repeated launches: the schedule counters must reset themselves
         again = _run(fpn, feats)
         for a, b in zip(fused, again):
             assert torch.equal(a, b)
     assert fpn.device_status() == 0
+
+
+@pytest.mark.parametrize("fused", [False, True])
+def test_both_schedules_match_oracle_swin_odd(cuda_device, fused):
+    import unified_fpn as U
+    chans, sizes = O.SWIN_CHANNELS, [(100, 167), (50, 84), (25, 42), (13, 21)]
+    feats = O.make_features(1, chans, sizes, seed=41, dist="normal")
+    wts = O.make_weights(chans, seed=42, bias_scale=0.1)
+    fpn = U.UnifiedFPN()
+    fpn.set_schedule(fused_neck_kernel=fused)
+    fpn.initialize_weights(wts.lat_w, wts.lat_b, wts.out_w, wts.out_b)
+    outs = _run(fpn, [_cl(f.to(torch.bfloat16).cuda()) for f in feats])
+    assert fpn.device_status() == 0
+    rw = O.NeckWeights([O.round_to(w, torch.bfloat16) for w in wts.lat_w], wts.lat_b,
+                       [O.round_to(w, torch.bfloat16) for w in wts.out_w], wts.out_b)
+    _check(outs, O.fpn_neck([O.round_to(f, torch.bfloat16) for f in feats], rw), TOL16)
 
 
 def test_neck_batch_linearity_and_sharding(cuda_device):
@@ -145,8 +165,10 @@ def test_autotune_and_cache(cuda_device, tmp_path):
     fpn2 = U.UnifiedFPN()
     fpn2.load_tuning(path)
     tuned = _run(fpn2, feats)
+    # Halo tiles sum K channel-block-major, plain tiles tap-major: the same values up to
+    # fp32 summation order, so tuned and untuned outputs agree within the bf16 tolerance.
     for a, b in zip(base, tuned):
-        assert O.rel_err(a.float().cpu(), b.float().cpu()) < 1e-6  # tiling changes nothing numerically
+        assert O.rel_err(a.float().cpu(), b.float().cpu()) < TOL16
 
 
 def test_errors_are_raised_not_exit(cuda_device):
