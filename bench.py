@@ -58,6 +58,24 @@ def neck_bytes(batch, chans, sizes, esz):
     return b
 
 
+def rank_images(rank, per_rank):
+    """Global image indices of a rank's batch slice (contiguous, per_rank images each)."""
+    return list(range(rank * per_rank, (rank + 1) * per_rank))
+
+
+def job_throughput(ms_local, images_local, world, device=None):
+    """Whole-job timing across ranks: (slowest rank's ms, images processed by all ranks).
+    The only collectives of a run; they sit outside the timed window."""
+    if world <= 1:
+        return float(ms_local), int(images_local)
+    import torch.distributed as dist
+    t = torch.tensor([float(ms_local)], dtype=torch.float64, device=device)
+    n = torch.tensor([float(images_local)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dist.all_reduce(n, op=dist.ReduceOp.SUM)
+    return float(t.item()), int(round(n.item()))
+
+
 def measured_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -264,13 +282,8 @@ def main():
     if world > 1:
         dist.barrier()
     clk = clocks.stop()
-    ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms, images = job_throughput(e0.elapsed_time(e1), B * args.steps, world, dev)
     status = fpn.device_status()
-    images = B * world * args.steps
     value = images / (ms / 1e3)
     ms_per_step = ms / args.steps
 
@@ -303,12 +316,8 @@ def main():
             e2e_step()
         a1.record(stream)
         torch.cuda.synchronize(dev)
-        ems = a0.elapsed_time(a1)
-        if world > 1:
-            t = torch.tensor([ems], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ems = float(t.item())
-        e2e = {"value": B * world * n_e2e / (ems / 1e3), "unit": "images/s", "h2d_bytes_per_step": h2d,
+        ems, e_images = job_throughput(a0.elapsed_time(a1), B * n_e2e, world, dev)
+        e2e = {"value": e_images / (ems / 1e3), "unit": "images/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "steps": n_e2e}
 
     # ---------------------------------------------------------------- roofline of the dominant kernel
