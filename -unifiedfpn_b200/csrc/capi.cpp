@@ -135,7 +135,8 @@ int ufpn_core_configure_levels(ufpn_core* core, int batch, const int* in_channel
   if (!core || !in_channels || !heights || !widths) return fail(UFPN_ERR_INVALID_ARG, "NULL");
   DType dt;
   Layout lay;
-  if (!parse_dtype(dtype, &dt)) return fail(UFPN_ERR_UNSUPPORTED, "unsupported dtype");
+  if (!parse_dtype(dtype, &dt) && dtype != UFPN_DTYPE_E4M3)
+    return fail(UFPN_ERR_UNSUPPORTED, "unsupported dtype");
   if (!parse_layout(layout, &lay)) return fail(UFPN_ERR_INVALID_ARG, "bad layout");
   return guarded([&] {
     std::vector<FPNDimensions> dims(4);
@@ -168,6 +169,17 @@ int ufpn_core_forward(ufpn_core* core, const void* const* inputs, void* const* o
   if (!core || !inputs || !outputs) return fail(UFPN_ERR_INVALID_ARG, "NULL");
   return guarded([&] {
     core->core.forward_raw(inputs, outputs, p6, static_cast<cudaStream_t>(stream));
+    return UFPN_OK;
+  });
+}
+
+int ufpn_core_forward_e4m3(ufpn_core* core, const void* const* inputs,
+                           const float* const* input_scales, void* const* outputs, void* p6,
+                           void* stream) {
+  if (!core || !inputs || !input_scales || !outputs) return fail(UFPN_ERR_INVALID_ARG, "NULL");
+  return guarded([&] {
+    core->core.forward_raw_scaled(inputs, input_scales, outputs, p6,
+                                  static_cast<cudaStream_t>(stream));
     return UFPN_OK;
   });
 }
@@ -394,6 +406,97 @@ int ufpn_layout_convert(int dtype, const void* in, void* out, int N, int C, int 
   cudaError_t e = ufpn::launch_transpose(dt, in, out, N, C, H * W, to_nhwc != 0,
                                          static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "layout convert");
+}
+
+// ------------------------------------------------------------------ e4m3 (FP8) path
+int ufpn_absmax(int dtype, const void* x, long long count, int groups, unsigned* amax_bits,
+                void* stream) {
+  DType dt;
+  if (!parse_dtype(dtype, &dt)) return fail(UFPN_ERR_UNSUPPORTED, "unsupported dtype");
+  if (!x || !amax_bits || count <= 0) return fail(UFPN_ERR_INVALID_ARG, "bad arguments");
+  if (groups < 1 || groups > 65535 || count % groups != 0)
+    return fail(UFPN_ERR_INVALID_ARG, "groups must divide count (1..65535 groups)");
+  cudaError_t e =
+      ufpn::launch_absmax(dt, x, count, groups, amax_bits, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "absmax");
+}
+
+int ufpn_quantize_e4m3(int dtype, const void* x, long long count, int groups, unsigned* amax_ws,
+                       void* q, float* scale_out, void* stream) {
+  DType dt;
+  if (!parse_dtype(dtype, &dt)) return fail(UFPN_ERR_UNSUPPORTED, "unsupported dtype");
+  if (!x || !amax_ws || !q || !scale_out || count <= 0)
+    return fail(UFPN_ERR_INVALID_ARG, "bad arguments");
+  if (groups < 1 || groups > 65535 || count % groups != 0)
+    return fail(UFPN_ERR_INVALID_ARG, "groups must divide count (1..65535 groups)");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(amax_ws, 0, sizeof(unsigned) * groups, s);
+  if (e == cudaSuccess) e = ufpn::launch_absmax(dt, x, count, groups, amax_ws, s);
+  if (e == cudaSuccess)
+    e = ufpn::launch_quantize_e4m3(dt, x, count, groups, amax_ws, q, scale_out, s);
+  return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "quantize e4m3");
+}
+
+int ufpn_quantize_e4m3_rows(const float* w, int rows, int cols, int pack_cin, void* q,
+                            float* scales, void* stream) {
+  if (!w || !q || !scales || rows <= 0 || cols <= 0 || pack_cin < 0)
+    return fail(UFPN_ERR_INVALID_ARG, "bad arguments");
+  if (pack_cin > 0 && cols != 9 * pack_cin)
+    return fail(UFPN_ERR_INVALID_ARG, "packing a 3x3 kernel needs cols == 9 * pack_cin");
+  cudaError_t e = ufpn::launch_quantize_rows_e4m3(w, rows, cols, pack_cin, q, scales,
+                                                  static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "quantize e4m3 rows");
+}
+
+int ufpn_lateral_conv_e4m3(const void* x, const float* x_scale, int x_scale_per_image,
+                           const void* w, const float* w_scales, const float* bias,
+                           const void* coarse, void* out, int N, int Cin, int H, int W, int Hc,
+                           int Wc, unsigned* amax_out, void* stream) {
+  if (!x || !x_scale || !w || !w_scales || !bias || !out)
+    return fail(UFPN_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (N <= 0 || Cin <= 0 || H <= 0 || W <= 0)
+    return fail(UFPN_ERR_INVALID_ARG, "sizes must be positive");
+  if (coarse && (Hc <= 0 || Wc <= 0 || Hc > H || Wc > W))
+    return fail(UFPN_ERR_INVALID_ARG, "coarse map must be non-empty and not larger than output");
+  if (Cin % 16 != 0) return fail(UFPN_ERR_UNSUPPORTED, "Cin must be a multiple of 16");
+  if (!ufpn::aligned16(x) || !ufpn::aligned16(w) || !ufpn::aligned16(out) ||
+      !ufpn::aligned16(bias) || !ufpn::aligned16(w_scales) ||
+      (coarse && !ufpn::aligned16(coarse)))
+    return fail(UFPN_ERR_ALIGNMENT, "tensors must be 16-byte aligned");
+  ufpn::TcScales sc;
+  sc.ascale = x_scale;
+  sc.ascale_per_image = x_scale_per_image != 0;
+  sc.wscale = w_scales;
+  sc.amax_out = amax_out;
+  ufpn::TcPlan plan;
+  cudaError_t e = ufpn::plan_tc_lateral(plan, DType::E4M3, x, w, bias, coarse, out, N, Cin, H, W,
+                                        coarse ? Hc : 0, coarse ? Wc : 0,
+                                        ufpn::default_tiling(H, W), device_status_word(), 0, sc);
+  if (e != cudaSuccess) return cuda_fail(e, "plan e4m3 lateral");
+  e = ufpn::launch_tc(plan, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "e4m3 lateral launch");
+}
+
+int ufpn_conv3x3_e4m3(const void* x, const float* x_scale, int x_scale_per_image, const void* w,
+                      const float* w_scales, const float* bias, void* out, void* p6, int N,
+                      int H, int W, unsigned* amax_out, void* stream) {
+  if (!x || !x_scale || !w || !w_scales || !bias || !out)
+    return fail(UFPN_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (N <= 0 || H <= 0 || W <= 0) return fail(UFPN_ERR_INVALID_ARG, "sizes must be positive");
+  if (!ufpn::aligned16(x) || !ufpn::aligned16(w) || !ufpn::aligned16(out) ||
+      !ufpn::aligned16(bias) || !ufpn::aligned16(w_scales) || (p6 && !ufpn::aligned16(p6)))
+    return fail(UFPN_ERR_ALIGNMENT, "tensors must be 16-byte aligned");
+  ufpn::TcScales sc;
+  sc.ascale = x_scale;
+  sc.ascale_per_image = x_scale_per_image != 0;
+  sc.wscale = w_scales;
+  sc.amax_out = amax_out;
+  ufpn::TcPlan plan;
+  cudaError_t e = ufpn::plan_tc_conv3x3(plan, DType::E4M3, x, w, bias, out, p6, N, H, W,
+                                        ufpn::halo_tiling(), device_status_word(), 0, sc);
+  if (e != cudaSuccess) return cuda_fail(e, "plan e4m3 conv3x3");
+  e = ufpn::launch_tc(plan, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "e4m3 conv3x3 launch");
 }
 
 // ------------------------------------------------------------------ reference C ABI

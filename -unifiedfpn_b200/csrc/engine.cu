@@ -55,8 +55,10 @@ DType to_dtype(FPNDataType t) {
       return DType::F16;
     case FPNDataType::BFLOAT16:
       return DType::BF16;
+    case FPNDataType::FP8_E4M3:
+      return DType::E4M3;
     default:
-      FPN_THROW("unsupported dtype: the neck runs in FLOAT32, FLOAT16 or BFLOAT16");
+      FPN_THROW("unsupported dtype: the neck runs in FLOAT32, FLOAT16, BFLOAT16 or FP8_E4M3");
   }
 }
 
@@ -92,8 +94,14 @@ struct UnifiedFPNCore::Impl {
   float* out_b[4] = {};
   void* lat_wp[4] = {};
   void* out_wp[4] = {};
+  float* lat_ws[4] = {};  // e4m3: per-output-channel weight scales
+  float* out_ws[4] = {};
   DType packed_dtype = DType::F32;
-  void* merged[4] = {};
+  void* merged[4] = {};   // M_l in the compute dtype (bf16 for e4m3 inputs)
+  void* qmerged[4] = {};  // e4m3: M_l quantised per tensor (input of the 3x3)
+  const float* in_scale[4] = {};  // e4m3: scales of the current forward's inputs
+  unsigned* fp8_amax = nullptr;   // e4m3: [4][N] per-image absmax of M_l (fp32 bits)
+  float* fp8_scale = nullptr;     // e4m3: [4][N] per-image dequantisation scale of M_l
   void* nhwc_in[4] = {};
   void* nhwc_out[5] = {};
   size_t workspace_bytes = 0;
@@ -117,6 +125,7 @@ struct UnifiedFPNCore::Impl {
   FPNPerformanceMetrics metrics{};
   struct GraphEntry {
     const void* in[4];
+    const float* scale[4];
     void* out[4];
     void* p6;
     cudaGraphExec_t exec;
@@ -134,13 +143,17 @@ struct UnifiedFPNCore::Impl {
   void free_workspace() {
     for (int l = 0; l < 4; ++l) {
       cudaFree(merged[l]);
+      cudaFree(qmerged[l]);
       cudaFree(nhwc_in[l]);
-      merged[l] = nhwc_in[l] = nullptr;
+      merged[l] = qmerged[l] = nhwc_in[l] = nullptr;
     }
     for (int l = 0; l < 5; ++l) {
       cudaFree(nhwc_out[l]);
       nhwc_out[l] = nullptr;
     }
+    cudaFree(fp8_amax);  // one allocation with fp8_scale
+    fp8_amax = nullptr;
+    fp8_scale = nullptr;
     workspace_bytes = 0;
   }
   void free_weights() {
@@ -151,7 +164,9 @@ struct UnifiedFPNCore::Impl {
       cudaFree(out_b[l]);
       cudaFree(lat_wp[l]);
       cudaFree(out_wp[l]);
-      lat_w32[l] = lat_b[l] = out_w32[l] = out_b[l] = nullptr;
+      cudaFree(lat_ws[l]);
+      cudaFree(out_ws[l]);
+      lat_w32[l] = lat_b[l] = out_w32[l] = out_b[l] = lat_ws[l] = out_ws[l] = nullptr;
       lat_wp[l] = out_wp[l] = nullptr;
       weights_set[l] = false;
     }
@@ -206,10 +221,17 @@ struct UnifiedFPNCore::Impl {
     for (int l = 0; l < 4; ++l) {
       cudaFree(lat_wp[l]);
       cudaFree(out_wp[l]);
+      cudaFree(lat_ws[l]);
+      cudaFree(out_ws[l]);
       lat_wp[l] = out_wp[l] = nullptr;
+      lat_ws[l] = out_ws[l] = nullptr;
       const size_t esz = ufpn::dtype_size(dtype);
       check(cudaMalloc(&lat_wp[l], static_cast<size_t>(cout) * w_cin[l] * esz), "cudaMalloc");
       check(cudaMalloc(&out_wp[l], static_cast<size_t>(cout) * cout * 9 * esz), "cudaMalloc");
+      if (dtype == DType::E4M3) {
+        check(cudaMalloc(&lat_ws[l], cout * sizeof(float)), "cudaMalloc");
+        check(cudaMalloc(&out_ws[l], cout * sizeof(float)), "cudaMalloc");
+      }
       if (weights_set[l]) pack_level(l);
     }
     packed_dtype = dtype;
@@ -217,6 +239,17 @@ struct UnifiedFPNCore::Impl {
 
   void pack_level(int l) {
     if (!tensor_core_path()) return;
+    if (dtype == DType::E4M3) {
+      // Per output channel: scale = absmax / 448, e4m3 codes; 3x3 packed tap-major.
+      check(ufpn::launch_quantize_rows_e4m3(lat_w32[l], cout, w_cin[l], 0, lat_wp[l], lat_ws[l],
+                                            setup),
+            "quantise lateral weights");
+      check(ufpn::launch_quantize_rows_e4m3(out_w32[l], cout, cout * 9, cout, out_wp[l],
+                                            out_ws[l], setup),
+            "quantise 3x3 weights");
+      check(cudaStreamSynchronize(setup), "weight quantisation");
+      return;
+    }
     check(ufpn::launch_convert_weights(dtype, lat_w32[l], lat_wp[l],
                                        static_cast<long long>(cout) * w_cin[l], setup),
           "pack lateral weights");
@@ -256,6 +289,7 @@ struct UnifiedFPNCore::Impl {
       return launches;
     }
 
+    if (dtype == DType::E4M3) return enqueue_e4m3(in, out, p6, main, prof_events);
     const bool nchw = layout == Layout::NCHW;
     const void* x[4];
     void* o[4];
@@ -386,6 +420,87 @@ struct UnifiedFPNCore::Impl {
     return launches;
   }
 
+  // e4m3 inputs (NHWC), bf16 M_l and outputs.  Same dependence structure as the 16-bit
+  // split schedule; each M_l additionally gets its per-image absmax from the kernel that
+  // writes it (P5 / P2 lateral epilogue, P4 / P3 merge) and is quantised to e4m3 per image
+  // on the side stream right before its 3x3 (per image, so an image's result does not
+  // depend on the rest of its batch, e.g. on how a batch is sharded over GPUs):
+  //   main:  zero amax | lat5 (amax5) lat4 lat3 | merge4 (amax4) | merge3 (amax3) | lat2 + up(M3) (amax2)
+  //   side:              q5 3x3_5 (+P6)        q4 3x3_4         q3 3x3_3          q2 3x3_2
+  int enqueue_e4m3(const void* const* in, void* const* out, void* p6, cudaStream_t main,
+                   bool prof_events) {
+    int launches = 0;
+    auto ok = [&](cudaError_t e, const char* what) {
+      check(e, what);
+      ++launches;
+    };
+    const cudaStream_t conv_stream = prof_events ? main : side;
+    if (prof_events) cudaEventRecord(prof[0], main);
+    check(cudaMemsetAsync(fp8_amax, 0, 4 * static_cast<size_t>(batch) * sizeof(unsigned), main),
+          "memset");
+    if (!prof_events) {
+      check(cudaEventRecord(ev_fork, main), "event");
+      check(cudaStreamWaitEvent(side, ev_fork, 0), "event");
+    }
+    auto lateral = [&](int l, const void* coarse, unsigned* amax_out) {
+      ufpn::TcScales sc;
+      sc.ascale = in_scale[l];
+      sc.wscale = lat_ws[l];
+      sc.amax_out = amax_out;
+      TcPlan p;
+      check(ufpn::plan_tc_lateral(p, DType::E4M3, in[l], lat_wp[l], lat_b[l], coarse, merged[l],
+                                  batch, cin[l], H[l], W[l], coarse ? H[l + 1] : 0,
+                                  coarse ? W[l + 1] : 0, ufpn::default_tiling(H[l], W[l]),
+                                  d_status, 0, sc),
+            "plan e4m3 lateral");
+      ok(ufpn::launch_tc(p, main), "e4m3 lateral launch");
+    };
+    auto conv_level = [&](int l) {
+      if (!prof_events) {
+        check(cudaEventRecord(ev_lat[l], main), "event");
+        check(cudaStreamWaitEvent(side, ev_lat[l], 0), "event");
+      }
+      const long long n = static_cast<long long>(batch) * H[l] * W[l] * cout;
+      ok(ufpn::launch_quantize_e4m3(DType::BF16, merged[l], n, batch, fp8_amax + l * batch,
+                                    qmerged[l], fp8_scale + l * batch, conv_stream),
+         "quantise merged map");
+      ufpn::TcScales sc;
+      sc.ascale = fp8_scale + l * batch;
+      sc.ascale_per_image = true;
+      sc.wscale = out_ws[l];
+      TcPlan conv;
+      check(ufpn::plan_tc_conv3x3(conv, DType::E4M3, qmerged[l], out_wp[l], out_b[l], out[l],
+                                  l == 3 ? p6 : nullptr, batch, H[l], W[l], ufpn::halo_tiling(),
+                                  d_status, 0, sc),
+            "plan e4m3 conv3x3");
+      ok(ufpn::launch_tc(conv, conv_stream), "e4m3 conv3x3 launch");
+    };
+    lateral(3, nullptr, fp8_amax + 3 * batch);
+    lateral(2, nullptr, nullptr);
+    lateral(1, nullptr, nullptr);
+    if (prof_events) cudaEventRecord(prof[1], main);
+    conv_level(3);
+    if (prof_events) cudaEventRecord(prof[2], main);
+    for (int l = 2; l >= 1; --l) {
+      ok(ufpn::launch_upsample_add(DType::BF16, merged[l + 1], merged[l], merged[l], batch, cout,
+                                   H[l + 1], W[l + 1], H[l], W[l], 0, Layout::NHWC, main,
+                                   fp8_amax + l * batch),
+         "merge");
+      if (prof_events) cudaEventRecord(prof[3 + 2 * (2 - l)], main);
+      conv_level(l);
+      if (prof_events) cudaEventRecord(prof[4 + 2 * (2 - l)], main);
+    }
+    lateral(0, merged[1], fp8_amax);
+    if (prof_events) cudaEventRecord(prof[7], main);
+    conv_level(0);
+    if (prof_events) cudaEventRecord(prof[8], main);
+    if (!prof_events) {
+      check(cudaEventRecord(ev_join, side), "event");
+      check(cudaStreamWaitEvent(main, ev_join, 0), "event");
+    }
+    return launches;
+  }
+
   double flops() const {
     double f = 0;
     for (int l = 0; l < 4; ++l) {
@@ -395,11 +510,12 @@ struct UnifiedFPNCore::Impl {
     return f;
   }
   double compulsory_bytes() const {
-    const double esz = ufpn::dtype_size(dtype);
+    const double esz = ufpn::dtype_size(dtype);              // inputs and weights
+    const double osz = dtype == DType::E4M3 ? 2.0 : esz;     // outputs (bf16 for e4m3)
     double b = 0;
     for (int l = 0; l < 4; ++l) {
       const double px = static_cast<double>(batch) * H[l] * W[l];
-      b += px * cin[l] * esz + px * cout * esz;              // read C_l, write P_l
+      b += px * cin[l] * esz + px * cout * osz;              // read C_l, write P_l
       b += (static_cast<double>(cout) * cin[l] + 9.0 * cout * cout) * esz;  // weights
     }
     return b;
@@ -437,13 +553,15 @@ void UnifiedFPNCore::configure_levels(const std::vector<FPNDimensions>& dims, in
   const Layout lay = layout == FPNLayout::NHWC ? Layout::NHWC : Layout::NCHW;
   if (dt == DType::F32 && lay != Layout::NCHW)
     FPN_THROW("the fp32 path takes NCHW (contiguous) tensors");
+  if (dt == DType::E4M3 && lay != Layout::NHWC)
+    FPN_THROW("FP8_E4M3 inputs must be NHWC (channels_last)");
   const int N = dims[0].batch_size;
   for (int l = 0; l < 4; ++l) {
     if (dims[l].batch_size != N) FPN_THROW("all levels must share the batch size");
     if (dims[l].channels <= 0 || dims[l].height <= 0 || dims[l].width <= 0)
       FPN_THROW("level dimensions must be positive");
-    if (dt != DType::F32 && dims[l].channels % 8 != 0)
-      FPN_THROW("16-bit inputs need Cin % 8 == 0 (16-byte TMA row stride)");
+    if (dt != DType::F32 && (dims[l].channels * ufpn::dtype_size(dt)) % 16 != 0)
+      FPN_THROW("tensor-core inputs need Cin x element size % 16 == 0 (16-byte TMA row stride)");
     if (l < 3 && (dims[l + 1].height > dims[l].height || dims[l + 1].width > dims[l].width))
       FPN_THROW("levels must be ordered fine (C2) to coarse (C5)");
   }
@@ -471,16 +589,27 @@ void UnifiedFPNCore::configure_levels(const std::vector<FPNDimensions>& dims, in
     }
   }
   const size_t esz = ufpn::dtype_size(dt);
+  const size_t msz = dt == DType::E4M3 ? 2 : esz;  // merged maps: bf16 for e4m3 inputs
   size_t total = 0;
   for (int l = 0; l < 4; ++l) {
     const size_t px = static_cast<size_t>(N) * m.H[l] * m.W[l];
-    m.check(cudaMalloc(&m.merged[l], px * m.cout * esz), "workspace");
-    total += px * m.cout * esz;
+    m.check(cudaMalloc(&m.merged[l], px * m.cout * msz), "workspace");
+    total += px * m.cout * msz;
+    if (dt == DType::E4M3) {
+      m.check(cudaMalloc(&m.qmerged[l], px * m.cout), "workspace");
+      total += px * m.cout;
+    }
     if (m.tensor_core_path() && lay == Layout::NCHW) {
       m.check(cudaMalloc(&m.nhwc_in[l], px * m.cin[l] * esz), "workspace");
       m.check(cudaMalloc(&m.nhwc_out[l], px * m.cout * esz), "workspace");
       total += px * (m.cin[l] + m.cout) * esz;
     }
+  }
+  if (dt == DType::E4M3) {
+    const size_t words = 4 * static_cast<size_t>(N);
+    m.check(cudaMalloc(&m.fp8_amax, 2 * words * sizeof(float)), "workspace");
+    m.fp8_scale = reinterpret_cast<float*>(m.fp8_amax + words);
+    total += 2 * words * sizeof(float);
   }
   if (m.tensor_core_path() && lay == Layout::NCHW) {
     const size_t px6 = static_cast<size_t>(N) * ((m.H[3] - 1) / 2 + 1) * ((m.W[3] - 1) / 2 + 1);
@@ -548,12 +677,28 @@ void UnifiedFPNCore::set_weights(int level, const float* lw, const float* lb, co
 
 void UnifiedFPNCore::forward_raw(const void* const* in, void* const* out, void* p6,
                                  cudaStream_t stream) {
+  forward_raw_scaled(in, nullptr, out, p6, stream);
+}
+
+void UnifiedFPNCore::forward_raw_scaled(const void* const* in, const float* const* scales,
+                                        void* const* out, void* p6, cudaStream_t stream) {
   Impl& m = *impl_;
   if (!m.configured) FPN_THROW("configure_levels() has not been called");
   for (int l = 0; l < 4; ++l) {
     if (!m.weights_set[l]) FPN_THROW("Weights not initialized");
     if (m.w_cin[l] != m.cin[l]) FPN_THROW("weights were allocated for different channel counts");
     if (!in[l] || !out[l]) FPN_THROW("null input/output pointer");
+  }
+  if (m.dtype == DType::E4M3) {
+    if (!scales) FPN_THROW("FP8_E4M3 inputs need their per-tensor scales");
+    if (!m.cfg.use_tensor_cores) FPN_THROW("FP8_E4M3 inputs run on the tensor cores only");
+    for (int l = 0; l < 4; ++l) {
+      if (!scales[l]) FPN_THROW("null input scale pointer");
+      m.in_scale[l] = scales[l];
+    }
+  } else {
+    if (scales) FPN_THROW("input scales apply to FP8_E4M3 inputs only");
+    for (int l = 0; l < 4; ++l) m.in_scale[l] = nullptr;
   }
   DeviceGuard g(m.device);
   m.ensure_weight_packing();
@@ -595,7 +740,8 @@ void UnifiedFPNCore::forward_raw(const void* const* in, void* const* out, void* 
     for (auto& e : m.graphs) {
       if (e.p6 != p6) continue;
       bool hit = true;
-      for (int l = 0; l < 4 && hit; ++l) hit = e.in[l] == in[l] && e.out[l] == out[l];
+      for (int l = 0; l < 4 && hit; ++l)
+        hit = e.in[l] == in[l] && e.out[l] == out[l] && e.scale[l] == m.in_scale[l];
       if (hit) {
         m.check(cudaGraphLaunch(e.exec, stream), "cudaGraphLaunch");
         m.metrics.num_kernel_launches = e.launches;
@@ -627,6 +773,7 @@ void UnifiedFPNCore::forward_raw(const void* const* in, void* const* out, void* 
     for (int l = 0; l < 4; ++l) {
       e.in[l] = in[l];
       e.out[l] = out[l];
+      e.scale[l] = m.in_scale[l];
     }
     e.p6 = p6;
     e.exec = exec;
@@ -706,6 +853,10 @@ std::string UnifiedFPNCore::autotune(const void* const* in, void* const* out, vo
   std::ostringstream rep;
   if (!m.tensor_core_path()) {
     rep << "fp32 path: nothing to tune\n";
+    return rep.str();
+  }
+  if (m.dtype == DType::E4M3) {
+    rep << "e4m3 path: the 3x3 always uses the 8 x 16 halo tiling; nothing to tune\n";
     return rep.str();
   }
   DeviceGuard g(m.device);

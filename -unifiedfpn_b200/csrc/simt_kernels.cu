@@ -11,6 +11,7 @@
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 
 namespace ufpn {
 
@@ -79,6 +80,18 @@ struct Vec16 {
     T e[kN];
   };
 };
+
+// |v| as fp32 bits (orders like an unsigned integer).
+__device__ __forceinline__ uint32_t abs_bits(float v) { return __float_as_uint(v) & 0x7FFFFFFFu; }
+
+// Warp-reduced atomicMax that skips the atomic when the published value is already as
+// large (most warps, once the running maximum has settled), so one hot address sees
+// few atomics.  Every lane of the warp must call it.
+__device__ __forceinline__ void publish_amax(unsigned* amax, unsigned bits) {
+  bits = __reduce_max_sync(0xffffffffu, bits);
+  if ((threadIdx.x & 31) == 0 && bits > *reinterpret_cast<volatile unsigned*>(amax))
+    atomicMax(amax, bits);
+}
 
 // ---------------------------------------------------------------- NHWC upsample-add
 // out[n,y,x,c] = lat[n,y,x,c] (or 0) + bilinear(coarse)[n,y,x,c].
@@ -172,17 +185,26 @@ __global__ void __launch_bounds__(256) upsample_add_nhwc_kernel(
 // warp per output pixel, lane = 16 bytes (8 channels), a block = 8 consecutive pixels of
 // one row, no loops; all five loads of a lane are independent and issued back to back.
 // `out` may alias `lat` (each lane reads its lateral vector before writing it).
+// amax (optional): amax[n] = atomicMax of |out| of image n as fp32 bits (for a following
+// per-image e4m3 quantisation).
 template <typename T>
 __global__ void __launch_bounds__(256) upsample_add_px512_kernel(
     const T* __restrict__ coarse, const T* lat, T* out, int N, int Hc, int Wc, int H, int W,
-    int chunks, float sy_scale, float sx_scale, int ac) {
+    int chunks, float sy_scale, float sx_scale, int ac, unsigned* amax) {
   static_assert(sizeof(T) == 2, "16-bit types");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  unsigned m = 0;
+  int m_img = -1;  // image the running maximum m belongs to (block-uniform)
   for (long long u = blockIdx.x; u < static_cast<long long>(N) * H * chunks; u += gridDim.x) {
     const int r = static_cast<int>(u / chunks);
+    const int n = r / H;
+    if (amax && n != m_img) {
+      if (m_img >= 0) publish_amax(amax + m_img, m);
+      m = 0;
+      m_img = n;
+    }
     const int x = static_cast<int>(u - static_cast<long long>(r) * chunks) * 8 + warp;
     if (x >= W) continue;
-    const int n = r / H;
     const int y = r - n * H;
     const float sy = src_coord(y, Hc, H, sy_scale, ac);
     const float sx = src_coord(x, Wc, W, sx_scale, ac);
@@ -208,9 +230,11 @@ __global__ void __launch_bounds__(256) upsample_add_px512_kernel(
       v = fmaf(to_f(c.e[e]), w10, v);
       v = fmaf(to_f(d.e[e]), w11, v);
       o.e[e] = from_f<T>(v);
+      m = max(m, abs_bits(to_f(o.e[e])));
     }
     *reinterpret_cast<uint4*>(out + io) = o.u;
   }
+  if (amax && m_img >= 0) publish_amax(amax + m_img, m);
 }
 
 // ---------------------------------------------------------------- NCHW upsample-add
@@ -348,6 +372,117 @@ __global__ void pack_conv3x3_kernel(const float* __restrict__ in, T* __restrict_
   }
 }
 
+// ---------------------------------------------------------------- e4m3 quantisation
+// Symmetric e4m3 with scale = amax / 448 (per tensor for activations, per output
+// channel for weights):
+//   amax > 0:  inv = 448 / amax,  scale = amax / 448;   amax == 0: inv = scale = 1
+//   q = e4m3(x * inv), rounded to nearest even, saturated to +-448
+// Every step is one correctly rounded fp32 operation, so a CPU restatement reproduces
+// q and scale bit for bit.  The absmax travels as the bit pattern of a non-negative
+// fp32, which orders like an unsigned integer (atomicMax).
+__device__ __forceinline__ float e4m3_inv(unsigned amax_bits) {
+  const float a = __uint_as_float(amax_bits);
+  return a > 0.f ? __fdiv_rn(448.f, a) : 1.f;
+}
+__device__ __forceinline__ float e4m3_scale(unsigned amax_bits) {
+  const float a = __uint_as_float(amax_bits);
+  return a > 0.f ? __fdiv_rn(a, 448.f) : 1.f;
+}
+__device__ __forceinline__ uint32_t e4m3x4(float a, float b, float c, float d, float inv) {
+  const uint32_t lo =
+      __nv_cvt_float2_to_fp8x2(make_float2(a * inv, b * inv), __NV_SATFINITE, __NV_E4M3);
+  const uint32_t hi =
+      __nv_cvt_float2_to_fp8x2(make_float2(c * inv, d * inv), __NV_SATFINITE, __NV_E4M3);
+  return lo | (hi << 16);
+}
+
+// amax[g] = max |x| over group g = elements [g * per, (g + 1) * per).  Grid y = group;
+// 16-byte vectors when the group start is aligned (vec), then the tail.
+template <typename T>
+__global__ void __launch_bounds__(256) absmax_kernel(const T* __restrict__ x, long long per,
+                                                     int vec, unsigned* amax) {
+  constexpr int V = Vec16<T>::kN;
+  const T* xg = x + static_cast<long long>(blockIdx.y) * per;
+  unsigned m = 0;
+  const long long tid = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  const long long nv = vec ? per / V : 0;
+  for (long long i = tid; i < nv; i += stride) {
+    Vec16<T> v;
+    v.u = __ldg(reinterpret_cast<const uint4*>(xg) + i);
+#pragma unroll
+    for (int e = 0; e < V; ++e) m = max(m, abs_bits(to_f(v.e[e])));
+  }
+  for (long long i = nv * V + tid; i < per; i += stride) m = max(m, abs_bits(to_f(xg[i])));
+  publish_amax(amax + blockIdx.y, m);
+}
+
+// q = e4m3(x * inv) per element, inv from the absmax of the element's group (grid y);
+// block (0, g) also writes the group's dequantisation scale.
+template <typename T>
+__global__ void __launch_bounds__(256) quantize_e4m3_kernel(const T* __restrict__ x, long long per,
+                                                            int vec, const unsigned* amax,
+                                                            uint8_t* __restrict__ q,
+                                                            float* scale_out) {
+  const unsigned a = amax[blockIdx.y];
+  const float inv = e4m3_inv(a);
+  if (scale_out && blockIdx.x == 0 && threadIdx.x == 0) scale_out[blockIdx.y] = e4m3_scale(a);
+  x += static_cast<long long>(blockIdx.y) * per;
+  q += static_cast<long long>(blockIdx.y) * per;
+  const long long n = per;
+  const long long tid = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  // 8 elements (8 output bytes) per step when x is 16-byte and q 8-byte aligned.
+  const long long n8 = vec ? n / 8 : 0;
+  for (long long i = tid; i < n8; i += stride) {
+    float f[8];
+    if constexpr (sizeof(T) == 4) {
+      const float4 u = __ldg(reinterpret_cast<const float4*>(x) + 2 * i);
+      const float4 w = __ldg(reinterpret_cast<const float4*>(x) + 2 * i + 1);
+      f[0] = u.x; f[1] = u.y; f[2] = u.z; f[3] = u.w;
+      f[4] = w.x; f[5] = w.y; f[6] = w.z; f[7] = w.w;
+    } else {
+      Vec16<T> v;
+      v.u = __ldg(reinterpret_cast<const uint4*>(x) + i);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] = to_f(v.e[e]);
+    }
+    uint2 o;
+    o.x = e4m3x4(f[0], f[1], f[2], f[3], inv);
+    o.y = e4m3x4(f[4], f[5], f[6], f[7], inv);
+    reinterpret_cast<uint2*>(q)[i] = o;
+  }
+  for (long long i = n8 * 8 + tid; i < n; i += stride)
+    q[i] = static_cast<uint8_t>(
+        __nv_cvt_float_to_fp8(to_f(x[i]) * inv, __NV_SATFINITE, __NV_E4M3));
+}
+
+// Weights, one block per output channel (row): scale[row] = amax_row / 448 and
+// q = e4m3(w * 448 / amax_row).  pack_cin > 0: the row is [pack_cin][3][3] and q is
+// written tap-major, [9][pack_cin] (the K order of the 3x3 implicit GEMM).
+__global__ void __launch_bounds__(256) quantize_rows_e4m3_kernel(const float* __restrict__ w,
+                                                                 int cols, int pack_cin,
+                                                                 uint8_t* __restrict__ q,
+                                                                 float* __restrict__ scales) {
+  __shared__ unsigned red[8];
+  const float* row = w + static_cast<size_t>(blockIdx.x) * cols;
+  unsigned m = 0;
+  for (int i = threadIdx.x; i < cols; i += blockDim.x) m = max(m, abs_bits(row[i]));
+  m = __reduce_max_sync(0xffffffffu, m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  unsigned a = 0;
+  for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) a = max(a, red[i]);
+  const float inv = e4m3_inv(a);
+  if (threadIdx.x == 0) scales[blockIdx.x] = e4m3_scale(a);
+  uint8_t* qrow = q + static_cast<size_t>(blockIdx.x) * cols;
+  for (int i = threadIdx.x; i < cols; i += blockDim.x) {
+    const int dst = pack_cin > 0 ? (i % 9) * pack_cin + i / 9 : i;
+    qrow[dst] =
+        static_cast<uint8_t>(__nv_cvt_float_to_fp8(row[i] * inv, __NV_SATFINITE, __NV_E4M3));
+  }
+}
+
 // ---------------------------------------------------------------- fp32 CUDA-core GEMMs
 // out[n, o, p] = sum_k Wt[o, k] * B(n, k, p) + bias[o] (+ bilinear(coarse)[n, o, p])
 // with B either the NCHW input itself (1x1 conv, k = c) or its on-the-fly
@@ -441,9 +576,29 @@ int grid_for(long long work, int threads) {
   return static_cast<int>(g);
 }
 
+// Blocks per group so the whole launch still covers about 16 blocks per SM.
+int group_blocks(long long per, int groups, int elems_per_thread) {
+  long long want = (per / elems_per_thread + 255) / 256;
+  const long long cap = (148LL * 16 + groups - 1) / groups;
+  if (want > cap) want = cap;
+  return want < 1 ? 1 : static_cast<int>(want);
+}
+
+template <typename T>
+cudaError_t absmax_t(const void* x, long long n, int groups, unsigned* amax, cudaStream_t s) {
+  if (groups < 1 || groups > 65535 || n % groups != 0) return cudaErrorInvalidValue;
+  const long long per = n / groups;
+  const int vec =
+      (aligned16(x) && (per * static_cast<long long>(sizeof(T))) % 16 == 0) ? 1 : 0;
+  const dim3 grid(group_blocks(per, groups, Vec16<T>::kN), groups);
+  absmax_kernel<T><<<grid, 256, 0, s>>>(static_cast<const T*>(x), per, vec, amax);
+  return cudaGetLastError();
+}
+
 template <typename T>
 cudaError_t upsample_add_t(const void* coarse, const void* lat, void* out, int N, int C, int Hc,
-                           int Wc, int H, int W, int ac, Layout layout, cudaStream_t s) {
+                           int Wc, int H, int W, int ac, Layout layout, cudaStream_t s,
+                           unsigned* amax) {
   const float sy = (ac && H > 1) ? static_cast<float>(Hc - 1) / (H - 1)
                                  : static_cast<float>(Hc) / H;
   const float sx = (ac && W > 1) ? static_cast<float>(Wc - 1) / (W - 1)
@@ -461,7 +616,7 @@ cudaError_t upsample_add_t(const void* coarse, const void* lat, void* out, int N
         const long long blocks = static_cast<long long>(N) * H * chunks;
         const int grid = blocks < (1LL << 30) ? static_cast<int>(blocks) : (1 << 30);
         upsample_add_px512_kernel<T>
-            <<<grid, 256, 0, s>>>(c, l, o, N, Hc, Wc, H, W, chunks, sy, sx, ac);
+            <<<grid, 256, 0, s>>>(c, l, o, N, Hc, Wc, H, W, chunks, sy, sx, ac, amax);
         return cudaGetLastError();
       }
     }
@@ -479,7 +634,10 @@ cudaError_t upsample_add_t(const void* coarse, const void* lat, void* out, int N
     upsample_add_nchw_kernel<T>
         <<<grid_for(work, 256), 256, 0, s>>>(c, l, o, N, C, Hc, Wc, H, W, sy, sx, ac);
   }
-  return cudaGetLastError();
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess && amax)
+    e = absmax_t<T>(out, static_cast<long long>(N) * C * H * W, N, amax, s);
+  return e;
 }
 
 template <typename T>
@@ -521,16 +679,17 @@ cudaError_t transpose_t(const void* in, void* out, int N, int C, int HW, bool to
 
 cudaError_t launch_upsample_add(DType dt, const void* coarse, const void* lat, void* out, int N,
                                 int C, int Hc, int Wc, int H, int W, int align_corners,
-                                Layout layout, cudaStream_t s) {
+                                Layout layout, cudaStream_t s, unsigned* amax_out) {
   switch (dt) {
     case DType::F32:
-      return upsample_add_t<float>(coarse, lat, out, N, C, Hc, Wc, H, W, align_corners, layout, s);
+      return upsample_add_t<float>(coarse, lat, out, N, C, Hc, Wc, H, W, align_corners, layout, s,
+                                   amax_out);
     case DType::F16:
       return upsample_add_t<__half>(coarse, lat, out, N, C, Hc, Wc, H, W, align_corners, layout,
-                                    s);
+                                    s, amax_out);
     case DType::BF16:
       return upsample_add_t<__nv_bfloat16>(coarse, lat, out, N, C, Hc, Wc, H, W, align_corners,
-                                           layout, s);
+                                           layout, s, amax_out);
     default:
       return cudaErrorInvalidValue;
   }
@@ -596,6 +755,62 @@ cudaError_t launch_pack_conv3x3(DType dt, const float* in, void* out, int Cout, 
     default:
       return cudaErrorInvalidValue;
   }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_absmax(DType dt, const void* x, long long n, int groups, unsigned* amax_bits,
+                          cudaStream_t s) {
+  if (n <= 0 || !x || !amax_bits) return cudaErrorInvalidValue;
+  switch (dt) {
+    case DType::F32:
+      return absmax_t<float>(x, n, groups, amax_bits, s);
+    case DType::F16:
+      return absmax_t<__half>(x, n, groups, amax_bits, s);
+    case DType::BF16:
+      return absmax_t<__nv_bfloat16>(x, n, groups, amax_bits, s);
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_quantize_e4m3(DType dt, const void* x, long long n, int groups,
+                                 const unsigned* amax_bits, void* q, float* scale_out,
+                                 cudaStream_t s) {
+  if (n <= 0 || !x || !q || !amax_bits) return cudaErrorInvalidValue;
+  if (groups < 1 || groups > 65535 || n % groups != 0) return cudaErrorInvalidValue;
+  const long long per = n / groups;
+  const int vec = (aligned16(x) && (reinterpret_cast<uintptr_t>(q) & 7u) == 0 && per % 8 == 0 &&
+                   (per * dtype_size(dt)) % 16 == 0)
+                      ? 1
+                      : 0;
+  const dim3 g(group_blocks(per, groups, 8), groups);
+  n = per;
+  uint8_t* qb = static_cast<uint8_t*>(q);
+  switch (dt) {
+    case DType::F32:
+      quantize_e4m3_kernel<float>
+          <<<g, 256, 0, s>>>(static_cast<const float*>(x), n, vec, amax_bits, qb, scale_out);
+      break;
+    case DType::F16:
+      quantize_e4m3_kernel<__half>
+          <<<g, 256, 0, s>>>(static_cast<const __half*>(x), n, vec, amax_bits, qb, scale_out);
+      break;
+    case DType::BF16:
+      quantize_e4m3_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(x), n, vec, amax_bits, qb, scale_out);
+      break;
+    default:
+      return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_rows_e4m3(const float* w, int rows, int cols, int pack_cin, void* q,
+                                      float* scales, cudaStream_t s) {
+  if (!w || !q || !scales || rows <= 0 || cols <= 0) return cudaErrorInvalidValue;
+  if (pack_cin > 0 && cols != 9 * pack_cin) return cudaErrorInvalidValue;
+  quantize_rows_e4m3_kernel<<<rows, 256, 0, s>>>(w, cols, pack_cin, static_cast<uint8_t*>(q),
+                                                 scales);
   return cudaGetLastError();
 }
 

@@ -30,6 +30,9 @@
 // bias, converts, writes a 128-byte swizzled staging tile and stores it with a TMA
 // tensor store (which also clips ragged tiles).
 //
+// Inputs are bf16, fp16 or e4m3 (kind::f8f6f4, 128 channels per 128-byte row, bf16
+// output scaled per tensor x per output channel); the accumulator is fp32 throughout.
+//
 // One CTA per SM (persistent, static round-robin over tiles):
 //   warp 0      : TMA producer (lane 0 issues; the whole warp builds Wb)
 //   warp 1      : TMEM allocator + tcgen05.mma issuer (one lane)
@@ -62,10 +65,49 @@ struct TcCfg {
 };
 static_assert(TcCfg::kSmemBytes <= 232448, "tc smem");
 
+// Operand element traits.  A k-block is one 128-byte swizzled row of channels:
+// 64 channels of a 16-bit type, 128 of e4m3.  Either way a k-block is 4 MMAs of
+// 32 bytes along K (K = 16 for kind::f16, 32 for kind::f8f6f4), so the shared-memory
+// layout, descriptors and TMA byte counts are the same for every input type.
+// e4m3 inputs produce bf16 outputs: acc * (activation scale * per-channel weight
+// scale) + bias.
+template <typename T>
+struct TcElem;
+template <>
+struct TcElem<__nv_bfloat16> {
+  using Out = __nv_bfloat16;
+  static constexpr bool kFp8 = false;
+  static constexpr uint32_t kFmt = 1;  // kind::f16 BF16
+};
+template <>
+struct TcElem<__half> {
+  using Out = __half;
+  static constexpr bool kFp8 = false;
+  static constexpr uint32_t kFmt = 0;  // kind::f16 F16
+};
+template <>
+struct TcElem<__nv_fp8_e4m3> {
+  using Out = __nv_bfloat16;
+  static constexpr bool kFp8 = true;
+  static constexpr uint32_t kFmt = 0;  // kind::f8f6f4 E4M3
+};
+template <typename T>
+constexpr int kKbElems = 128 / static_cast<int>(sizeof(T));  // channels per k-block
+constexpr int kMmaPerKb = 4;                                   // 32-byte K steps per k-block
+
+template <typename T>
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  if constexpr (TcElem<T>::kFp8)
+    tc_mma_f8(d_tmem, adesc, bdesc, idesc, accumulate);
+  else
+    tc_mma_f16(d_tmem, adesc, bdesc, idesc, accumulate);
+}
+
 struct TcGemmArgs {
   int num_tiles;
   int num_kb;      // taps * cin_blocks (main loop only)
-  int cin_blocks;  // ceil(Cin / 64)
+  int cin_blocks;  // ceil(Cin / channels per k-block)
   int N_img, H, W;
   int tile_w, tile_h, tiles_x, tiles_y;
   const float* bias;  // [256] fp32
@@ -78,6 +120,13 @@ struct TcGemmArgs {
   void* p6;
   int H6, W6;
   int* status;  // device status word (0 = ok)
+  // e4m3 inputs only: out = acc * (ascale[n * ascale_stride] * wscale[o]) + bias[o]
+  const float* ascale;  // activation scale(s), device: one (stride 0) or one per image (1)
+  int ascale_stride;
+  const float* wscale;  // per-output-channel weight scales [256]
+  // optional: amax_out[n] = atomicMax of |out| (fp32 bits) over image n's stored elements
+  // (the absmax a following per-image e4m3 quantisation of this output needs)
+  unsigned* amax_out;
 };
 
 template <typename T>
@@ -230,6 +279,8 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
                                             uint64_t* acce_bar, uint8_t* smem_stage,
                                             volatile int* abort_flag, int warp, int lane,
                                             bool bil_mma) {
+  using O = typename TcElem<T>::Out;
+  constexpr bool kFp8 = TcElem<T>::kFp8;
   const int ew = warp - 2;
   const int quarter = warp & 3;  // TMEM lanes 32*quarter..+31
   const int chalf = ew >> 2;     // output channels chalf*128 .. +127
@@ -250,6 +301,8 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
     const int py = y0 + row / tw;
     const int px = x0 + row % tw;
     const bool valid = (py < args.H) && (px < args.W);
+    const float ascale = kFp8 ? __ldg(args.ascale + n * args.ascale_stride) : 1.f;
+    uint32_t amax_bits = 0;  // max |stored value| of this thread in this tile (fp32 bits)
 
     // Fallback only: bilinear taps of the coarser merged map from global memory.
     TcTaps tp{};
@@ -259,7 +312,7 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
     const uint8_t* g11 = nullptr;
     if (taps_global) {
       tp = tc_taps(py, px, args.H, args.W, args.Hc, args.Wc, args.scale_y, args.scale_x);
-      const size_t rowb = static_cast<size_t>(kTcBlockN) * sizeof(T);
+      const size_t rowb = static_cast<size_t>(kTcBlockN) * sizeof(O);
       const uint8_t* cbase = static_cast<const uint8_t*>(args.coarse) +
                              static_cast<size_t>(n) * args.Hc * args.Wc * rowb;
       g00 = cbase + (static_cast<size_t>(tp.ya) * args.Wc + tp.xa) * rowb;
@@ -273,7 +326,7 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
     if (emit_p6) {
       const size_t p6pix =
           (static_cast<size_t>(n) * args.H6 + (py >> 1)) * args.W6 + (px >> 1);
-      p6_row = static_cast<uint8_t*>(args.p6) + p6pix * kTcBlockN * sizeof(T);
+      p6_row = static_cast<uint8_t*>(args.p6) + p6pix * kTcBlockN * sizeof(O);
     }
     // Output box of this warp's 32 rows.
     const int wrow0 = quarter * 32;
@@ -298,16 +351,29 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
       }
       float v[64];
       const float4* b4 = reinterpret_cast<const float4*>(args.bias + col0);
+      if constexpr (kFp8) {
+        const float4* s4 = reinterpret_cast<const float4*>(args.wscale + col0);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float4 bb = __ldg(b4 + i);
-        v[4 * i + 0] = __uint_as_float(r[4 * i + 0]) + bb.x;
-        v[4 * i + 1] = __uint_as_float(r[4 * i + 1]) + bb.y;
-        v[4 * i + 2] = __uint_as_float(r[4 * i + 2]) + bb.z;
-        v[4 * i + 3] = __uint_as_float(r[4 * i + 3]) + bb.w;
+        for (int i = 0; i < 16; ++i) {
+          const float4 bb = __ldg(b4 + i);
+          const float4 ss = __ldg(s4 + i);
+          v[4 * i + 0] = fmaf(__uint_as_float(r[4 * i + 0]), ascale * ss.x, bb.x);
+          v[4 * i + 1] = fmaf(__uint_as_float(r[4 * i + 1]), ascale * ss.y, bb.y);
+          v[4 * i + 2] = fmaf(__uint_as_float(r[4 * i + 2]), ascale * ss.z, bb.z);
+          v[4 * i + 3] = fmaf(__uint_as_float(r[4 * i + 3]), ascale * ss.w, bb.w);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float4 bb = __ldg(b4 + i);
+          v[4 * i + 0] = __uint_as_float(r[4 * i + 0]) + bb.x;
+          v[4 * i + 1] = __uint_as_float(r[4 * i + 1]) + bb.y;
+          v[4 * i + 2] = __uint_as_float(r[4 * i + 2]) + bb.z;
+          v[4 * i + 3] = __uint_as_float(r[4 * i + 3]) + bb.w;
+        }
       }
       if (taps_global) {
-        const size_t off = static_cast<size_t>(col0) * sizeof(T);
+        const size_t off = static_cast<size_t>(col0) * sizeof(O);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const uint4 a = __ldg(reinterpret_cast<const uint4*>(g00 + off) + j);
@@ -320,10 +386,10 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
           const uint32_t du[4] = {d.x, d.y, d.z, d.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const float2 fa = Pack<T>::unpack(au[e]);
-            const float2 fb = Pack<T>::unpack(bu[e]);
-            const float2 fc = Pack<T>::unpack(cu[e]);
-            const float2 fd = Pack<T>::unpack(du[e]);
+            const float2 fa = Pack<O>::unpack(au[e]);
+            const float2 fb = Pack<O>::unpack(bu[e]);
+            const float2 fc = Pack<O>::unpack(cu[e]);
+            const float2 fd = Pack<O>::unpack(du[e]);
             v[8 * j + 2 * e + 0] += tp.w00 * fa.x + tp.w01 * fb.x + tp.w10 * fc.x + tp.w11 * fd.x;
             v[8 * j + 2 * e + 1] += tp.w00 * fa.y + tp.w01 * fb.y + tp.w10 * fc.y + tp.w11 * fd.y;
           }
@@ -335,13 +401,23 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         uint4 o;
-        o.x = Pack<T>::pack(v[8 * j + 0], v[8 * j + 1]);
-        o.y = Pack<T>::pack(v[8 * j + 2], v[8 * j + 3]);
-        o.z = Pack<T>::pack(v[8 * j + 4], v[8 * j + 5]);
-        o.w = Pack<T>::pack(v[8 * j + 6], v[8 * j + 7]);
+        o.x = Pack<O>::pack(v[8 * j + 0], v[8 * j + 1]);
+        o.y = Pack<O>::pack(v[8 * j + 2], v[8 * j + 3]);
+        o.z = Pack<O>::pack(v[8 * j + 4], v[8 * j + 5]);
+        o.w = Pack<O>::pack(v[8 * j + 6], v[8 * j + 7]);
+        if (args.amax_out != nullptr && valid) {
+          // max |x| of the rounded 16-bit values: clear the sign bits, then compare as
+          // unsigned (order-preserving for non-negative floats of one format).
+          const uint32_t w4[4] = {o.x, o.y, o.z, o.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = Pack<O>::unpack(w4[e] & 0x7FFF7FFFu);
+            amax_bits = max(amax_bits, max(__float_as_uint(f.x), __float_as_uint(f.y)));
+          }
+        }
         st_shared_v4(stage_addr + lane * 128 + ((j ^ (lane & 7)) << 4), o);
         if (emit_p6)
-          reinterpret_cast<uint4*>(p6_row + static_cast<size_t>(col0) * sizeof(T))[j] = o;
+          reinterpret_cast<uint4*>(p6_row + static_cast<size_t>(col0) * sizeof(O))[j] = o;
       }
       fence_proxy_async_smem();
       __syncwarp();
@@ -349,6 +425,12 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
         tma_store_4d(map_out, smem_stage + ew * kTcStagingPerWarp, col0, ox, oy, n);
         bulk_commit_group();
       }
+    }
+    if (args.amax_out != nullptr) {
+      // One atomic per warp and tile at most, skipped once the image's maximum is larger.
+      amax_bits = __reduce_max_sync(0xffffffffu, amax_bits);
+      if (lane == 0 && amax_bits > *reinterpret_cast<volatile unsigned*>(args.amax_out + n))
+        atomicMax(args.amax_out + n, amax_bits);
     }
     if (++acc == 2) {
       acc = 0;
@@ -384,7 +466,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   // Top-down add through the tensor core (coarse box fits one k-block).
-  const bool bil_mma = (kMode == 0) && args.coarse != nullptr && args.cbox_w > 0;
+  // (16-bit inputs only: the e4m3 epilogue scales the accumulator, which must then
+  // not already hold the unscaled top-down term.)
+  const bool bil_mma =
+      (kMode == 0) && !TcElem<T>::kFp8 && args.coarse != nullptr && args.cbox_w > 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -440,16 +525,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               dy = tap / 3 - 1;
               dx = tap % 3 - 1;
             }
-            tma_load_4d(smem_a + stage * kTcAStage, &map_a, &full_bar[stage], cb * kTcBlockK,
+            tma_load_4d(smem_a + stage * kTcAStage, &map_a, &full_bar[stage], cb * kKbElems<T>,
                         x0 + dx, y0 + dy, n,
                         kMode == 0 ? kPolicyEvictFirst : kPolicyEvictLast);
-            tma_load_2d(smem_b + stage * kTcBStage, &map_b, &full_bar[stage], kb * kTcBlockK, 0,
+            tma_load_2d(smem_b + stage * kTcBStage, &map_b, &full_bar[stage], kb * kKbElems<T>, 0,
                         kPolicyEvictLast);
           }
         } else {
           // Bilinear k-block: Wb into the A stage (generic stores, whole warp), the
           // coarse box into the B stage (TMA), then one arrival with the TMA bytes.
-          tc_build_bilinear<T>(smem_a + stage * kTcAStage, smem_b + stage * kTcBStage, lane,
+          tc_build_bilinear<typename TcElem<T>::Out>(smem_a + stage * kTcAStage, smem_b + stage * kTcBStage, lane,
                                x0, y0, args.tile_w, args.H, args.W, args.Hc, args.Wc,
                                args.scale_y, args.scale_x, args.cbox_w, args.cbox_h);
           fence_proxy_async_smem();
@@ -484,9 +569,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc(kTcBlockM, kTcBlockN, Pack<T>::kFmt, Pack<T>::kFmt);
-      constexpr uint32_t idesc_bmn =
-          make_idesc(kTcBlockM, kTcBlockN, Pack<T>::kFmt, Pack<T>::kFmt, 1u);
+      constexpr uint32_t idesc =
+          make_idesc(kTcBlockM, kTcBlockN, TcElem<T>::kFmt, TcElem<T>::kFmt);
+      // bilinear k-block: Wb and the coarse box are the 16-bit output type
+      constexpr uint32_t kOutFmt = TcElem<typename TcElem<T>::Out>::kFmt;
+      constexpr uint32_t idesc_bmn = make_idesc(kTcBlockM, kTcBlockN, kOutFmt, kOutFmt, 1u);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -508,9 +595,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           if (kb < args.num_kb) {
             const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(smem_b + stage * kTcBStage));
 #pragma unroll
-            for (int k = 0; k < kTcBlockK / 16; ++k) {
-              // +32 bytes along K per 16-element MMA step (encoded >> 4).
-              tc_mma_f16(d_tmem, adesc + 2u * k, bdesc + 2u * k, idesc,
+            for (int k = 0; k < kMmaPerKb; ++k) {
+              // +32 bytes along K per MMA step (encoded >> 4).
+              tc_mma<T>(d_tmem, adesc + 2u * k, bdesc + 2u * k, idesc,
                          (kb > 0 || k > 0) ? 1u : 0u);
             }
           } else {
@@ -519,7 +606,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const uint64_t bdesc =
                 sdesc_mnmajor_sw128(smem_u32(smem_b + stage * kTcBStage), kTcCoarseMaxPix * 128);
 #pragma unroll
-            for (int k = 0; k < kTcBlockK / 16; ++k)
+            for (int k = 0; k < kMmaPerKb; ++k)
               tc_mma_f16(d_tmem, adesc + 2u * k, bdesc + 128u * k, idesc_bmn, 1u);
           }
           tc_commit(&empty_bar[stage]);
@@ -664,7 +751,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             break;
           }
           mbar_arrive_expect_tx(&hfull_bar[hb], kHaloRows * 128);
-          tma_load_4d(smem_halo + hb * kHaloBytes, &map_a, &hfull_bar[hb], cb * kTcBlockK, x0 - 1,
+          tma_load_4d(smem_halo + hb * kHaloBytes, &map_a, &hfull_bar[hb], cb * kKbElems<T>, x0 - 1,
                       y0 - 1, n, kPolicyEvictLast);
           ++hissued;
           if (++hb == kHaloBufs) {
@@ -679,7 +766,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             mbar_arrive_expect_tx(&full_bar[stage], kTcBStage);
             tma_load_2d(smem_b + stage * kTcBStage, &map_b, &full_bar[stage],
-                        tap * (cin_blocks * kTcBlockK) + cb * kTcBlockK, 0, kPolicyEvictLast);
+                        (tap * cin_blocks + cb) * kKbElems<T>, 0, kPolicyEvictLast);
             ++issued;
             if (++stage == S) {
               stage = 0;
@@ -706,7 +793,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc(kTcBlockM, kTcBlockN, Pack<T>::kFmt, Pack<T>::kFmt);
+      constexpr uint32_t idesc =
+          make_idesc(kTcBlockM, kTcBlockN, TcElem<T>::kFmt, TcElem<T>::kFmt);
       int stage = 0, hb = 0, acc = 0;
       uint32_t phase = 0, hphase = 0, acc_phase = 0;
       bool ok = true;
@@ -734,8 +822,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 (kHaloTileW + 2) * 128);
             const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(smem_b + stage * kTcBStage));
 #pragma unroll
-            for (int k = 0; k < kTcBlockK / 16; ++k)
-              tc_mma_f16(d_tmem, adesc + 2u * k, bdesc + 2u * k, idesc,
+            for (int k = 0; k < kMmaPerKb; ++k)
+              tc_mma<T>(d_tmem, adesc + 2u * k, bdesc + 2u * k, idesc,
                          (cb > 0 || tap > 0 || k > 0) ? 1u : 0u);
             tc_commit(&empty_bar[stage]);
             if (++stage == S) {

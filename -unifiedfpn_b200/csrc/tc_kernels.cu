@@ -64,24 +64,25 @@ cudaError_t encode(CUtensorMap* map, DType dt, int rank, const void* base, const
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-// NHWC activation map [N][H][W][C] with a (64, bw, bh, 1) box.
+// NHWC activation map [N][H][W][C] with a (one 128-byte row of channels, bw, bh, 1) box.
 cudaError_t encode_nhwc(CUtensorMap* map, DType dt, const void* base, int N, int H, int W, int C,
                         int bw, int bh) {
-  const uint64_t esz = 2;
+  const uint64_t esz = static_cast<uint64_t>(dtype_size(dt));
   uint64_t dims[4] = {static_cast<uint64_t>(C), static_cast<uint64_t>(W),
                       static_cast<uint64_t>(H), static_cast<uint64_t>(N)};
   uint64_t strides[3] = {static_cast<uint64_t>(C) * esz, static_cast<uint64_t>(W) * C * esz,
                          static_cast<uint64_t>(H) * W * C * esz};
-  uint32_t box[4] = {static_cast<uint32_t>(kTcBlockK), static_cast<uint32_t>(bw),
+  uint32_t box[4] = {static_cast<uint32_t>(128 / esz), static_cast<uint32_t>(bw),
                      static_cast<uint32_t>(bh), 1};
   return encode(map, dt, 4, base, dims, strides, box);
 }
 
-// Weights [256][K] K-major, (64, 256) box.
+// Weights [256][K] K-major, (one 128-byte row of K, 256) box.
 cudaError_t encode_weights(CUtensorMap* map, DType dt, const void* base, int K) {
+  const uint64_t esz = static_cast<uint64_t>(dtype_size(dt));
   uint64_t dims[2] = {static_cast<uint64_t>(K), kTcBlockN};
-  uint64_t strides[1] = {static_cast<uint64_t>(K) * 2};
-  uint32_t box[2] = {kTcBlockK, kTcBlockN};
+  uint64_t strides[1] = {static_cast<uint64_t>(K) * esz};
+  uint32_t box[2] = {static_cast<uint32_t>(128 / esz), kTcBlockN};
   return encode(map, dt, 2, base, dims, strides, box);
 }
 
@@ -198,12 +199,17 @@ Conv3x3Tiling default_tiling(int H, int W) {
 cudaError_t plan_tc_lateral(TcPlan& plan, DType dt, const void* x, const void* w,
                             const float* bias, const void* coarse, void* out, int N, int Cin,
                             int H, int W, int Hc, int Wc, Conv3x3Tiling tiling, int* status,
-                            int max_ctas) {
-  if (dt != DType::BF16 && dt != DType::F16) return cudaErrorInvalidValue;
-  if (Cin <= 0 || Cin % 8 != 0 || N <= 0 || H <= 0 || W <= 0) return cudaErrorInvalidValue;
+                            int max_ctas, const TcScales& sc) {
+  if (dt != DType::BF16 && dt != DType::F16 && dt != DType::E4M3) return cudaErrorInvalidValue;
+  const bool fp8 = dt == DType::E4M3;
+  const DType odt = fp8 ? DType::BF16 : dt;  // output / coarse element type
+  const int kb_elems = 128 / dtype_size(dt);
+  if (Cin <= 0 || (Cin * dtype_size(dt)) % 16 != 0 || N <= 0 || H <= 0 || W <= 0) return cudaErrorInvalidValue;
   if (!valid_tiling(tiling)) return cudaErrorInvalidValue;
   if (coarse && (Hc <= 0 || Wc <= 0)) return cudaErrorInvalidValue;
-  if (!aligned16(out) || (coarse && !aligned16(coarse)) || !aligned16(bias))
+  if (fp8 && (!sc.ascale || !sc.wscale)) return cudaErrorInvalidValue;
+  if (!aligned16(out) || (coarse && !aligned16(coarse)) || !aligned16(bias) ||
+      (fp8 && !aligned16(sc.wscale)))
     return cudaErrorMisalignedAddress;
   TcGemmArgs a;
   std::memset(&a, 0, sizeof(a));
@@ -211,15 +217,19 @@ cudaError_t plan_tc_lateral(TcPlan& plan, DType dt, const void* x, const void* w
   const long long tiles = static_cast<long long>(a.tiles_x) * a.tiles_y * N;
   if (tiles >= (1LL << 31)) return cudaErrorInvalidValue;
   a.num_tiles = static_cast<int>(tiles);
-  a.cin_blocks = (Cin + kTcBlockK - 1) / kTcBlockK;
+  a.cin_blocks = (Cin + kb_elems - 1) / kb_elems;
   a.num_kb = a.cin_blocks;
   a.bias = bias;
   a.status = status;
+  a.ascale = sc.ascale;
+  a.ascale_stride = sc.ascale_per_image ? 1 : 0;
+  a.wscale = sc.wscale;
+  a.amax_out = sc.amax_out;
   cudaError_t e = encode_nhwc(&plan.map_a, dt, x, N, H, W, Cin, tiling.tile_w, tiling.tile_h);
   if (e != cudaSuccess) return e;
   if ((e = encode_weights(&plan.map_b, dt, w, Cin)) != cudaSuccess) return e;
   const int sw = tiling.tile_w < 32 ? tiling.tile_w : 32;
-  if ((e = encode_nhwc(&plan.map_out, dt, out, N, H, W, kTcBlockN, sw, 32 / sw)) != cudaSuccess)
+  if ((e = encode_nhwc(&plan.map_out, odt, out, N, H, W, kTcBlockN, sw, 32 / sw)) != cudaSuccess)
     return e;
   plan.map_coarse = plan.map_out;  // unused unless a coarse map is staged
   if (coarse) {
@@ -229,10 +239,11 @@ cudaError_t plan_tc_lateral(TcPlan& plan, DType dt, const void* x, const void* w
     a.scale_y = static_cast<float>(Hc) / static_cast<float>(H);
     a.scale_x = static_cast<float>(Wc) / static_cast<float>(W);
     // Coarse box of the tensor-core top-down add: the exact span of the taps of any
-    // tile (replaying the device arithmetic); must fit one 64-pixel k-block.
+    // tile (replaying the device arithmetic); must fit one 64-pixel k-block.  (e4m3:
+    // the accumulator is scaled in the epilogue, so the taps are added there.)
     const int ch = coarse_span(H, tiling.tile_h, a.scale_y, Hc);
     const int cw = coarse_span(W, tiling.tile_w, a.scale_x, Wc);
-    if (ch * cw <= kTcCoarseMaxPix) {
+    if (!fp8 && ch * cw <= kTcCoarseMaxPix) {
       a.cbox_h = ch;
       a.cbox_w = cw;
       if ((e = encode_nhwc(&plan.map_coarse, dt, coarse, N, Hc, Wc, kTcBlockN, cw, ch)) !=
@@ -251,11 +262,16 @@ cudaError_t plan_tc_lateral(TcPlan& plan, DType dt, const void* x, const void* w
 
 cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w,
                             const float* bias, void* out, void* p6, int N, int H, int W,
-                            Conv3x3Tiling tiling, int* status, int max_ctas) {
-  if (dt != DType::BF16 && dt != DType::F16) return cudaErrorInvalidValue;
+                            Conv3x3Tiling tiling, int* status, int max_ctas,
+                            const TcScales& sc) {
+  if (dt != DType::BF16 && dt != DType::F16 && dt != DType::E4M3) return cudaErrorInvalidValue;
+  const bool fp8 = dt == DType::E4M3;
+  const DType odt = fp8 ? DType::BF16 : dt;
   if (!valid_tiling(tiling)) return cudaErrorInvalidValue;
   if (N <= 0 || H <= 0 || W <= 0) return cudaErrorInvalidValue;
-  if (!aligned16(out) || (p6 && !aligned16(p6)) || !aligned16(bias))
+  if (fp8 && (!sc.ascale || !sc.wscale || !tiling.halo)) return cudaErrorInvalidValue;
+  if (!aligned16(out) || (p6 && !aligned16(p6)) || !aligned16(bias) ||
+      (fp8 && !aligned16(sc.wscale)))
     return cudaErrorMisalignedAddress;
   const int C = kTcBlockN;
   TcGemmArgs a;
@@ -264,13 +280,17 @@ cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w
   const long long tiles = static_cast<long long>(a.tiles_x) * a.tiles_y * N;
   if (tiles >= (1LL << 31)) return cudaErrorInvalidValue;
   a.num_tiles = static_cast<int>(tiles);
-  a.cin_blocks = C / kTcBlockK;
+  a.cin_blocks = C / (128 / dtype_size(dt));
   a.num_kb = 9 * a.cin_blocks;
   a.bias = bias;
   a.p6 = p6;
   a.H6 = (H - 1) / 2 + 1;
   a.W6 = (W - 1) / 2 + 1;
   a.status = status;
+  a.ascale = sc.ascale;
+  a.ascale_stride = sc.ascale_per_image ? 1 : 0;
+  a.wscale = sc.wscale;
+  a.amax_out = sc.amax_out;
   const bool halo = tiling.halo;
   if (halo && (tiling.tile_w != kHaloTileW || tiling.tile_h != kHaloTileH))
     return cudaErrorInvalidValue;
@@ -281,7 +301,7 @@ cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w
   if (e != cudaSuccess) return e;
   if ((e = encode_weights(&plan.map_b, dt, w, 9 * C)) != cudaSuccess) return e;
   const int sw = tiling.tile_w < 32 ? tiling.tile_w : 32;
-  if ((e = encode_nhwc(&plan.map_out, dt, out, N, H, W, kTcBlockN, sw, 32 / sw)) != cudaSuccess)
+  if ((e = encode_nhwc(&plan.map_out, odt, out, N, H, W, kTcBlockN, sw, 32 / sw)) != cudaSuccess)
     return e;
   plan.map_coarse = plan.map_out;
   std::memcpy(plan.args, &a, sizeof(a));
@@ -453,6 +473,11 @@ cudaError_t launch_neck(const NeckPlan& plan, cudaStream_t s) {
 
 cudaError_t launch_tc(const TcPlan& plan, cudaStream_t s) {
   if (plan.grid <= 0) return cudaSuccess;
+  if (plan.dtype == DType::E4M3) {
+    if (plan.mode == 0) return launch_t<0, __nv_fp8_e4m3>(plan, s);
+    if (plan.mode == 2) return launch_halo_t<__nv_fp8_e4m3>(plan, s);
+    return cudaErrorInvalidValue;
+  }
   if (plan.mode == 0) {
     return plan.dtype == DType::BF16 ? launch_t<0, __nv_bfloat16>(plan, s)
                                      : launch_t<0, __half>(plan, s);

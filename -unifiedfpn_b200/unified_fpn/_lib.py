@@ -75,6 +75,17 @@ SIGNATURES = {
                 c_void_p]),
     "ufpn_p6_maxpool": (c_int, [c_int, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
     "ufpn_pack_conv3x3_weights": (c_int, [c_int, c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "ufpn_absmax": (c_int, [c_int, c_void_p, c_longlong, c_int, c_void_p, c_void_p]),
+    "ufpn_quantize_e4m3": (c_int, [c_int, c_void_p, c_longlong, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "ufpn_quantize_e4m3_rows": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
+    "ufpn_lateral_conv_e4m3": (
+        c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "ufpn_conv3x3_e4m3": (
+        c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                c_int, c_int, c_int, c_void_p, c_void_p]),
+    "ufpn_core_forward_e4m3": (
+        c_int, [c_void_p, POINTER(c_void_p), POINTER(c_void_p), POINTER(c_void_p), c_void_p, c_void_p]),
     "ufpn_neck_forward_noalloc": (
         c_int, [c_int, POINTER(c_void_p), POINTER(c_void_p), POINTER(c_void_p), POINTER(c_void_p),
                 POINTER(c_void_p), POINTER(c_void_p), c_void_p, c_int, POINTER(c_int), POINTER(c_int),

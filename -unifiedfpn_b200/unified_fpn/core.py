@@ -10,6 +10,8 @@ Differences from the reference (whose sources do not build as shipped):
     float16 or bfloat16, NCHW-contiguous or channels_last, and returns P2..P5
     (plus P6 = max_pool2d(P5, 1, 2) with ``return_p6=True``).  Outputs keep the
     inputs' memory format.
+  * float8_e4m3fn inputs (with per-tensor ``input_scales``) run the FP8 neck on the
+    e4m3 tensor cores and return bf16 channels_last outputs.
   * The neck is the standard one: lateral 1x1 + bias, top-down bilinear
     upsample (align_corners=False) + add, full 3x3 output conv + bias.
   * Weights left uninitialised are filled deterministically (Kaiming-normal,
@@ -25,7 +27,7 @@ import torch
 
 from . import _lib
 from ._lib import check, lib
-from .ops import _DT, _stream
+from .ops import _DT, E4M3, _stream
 
 _ACT = {"none": 0, "relu": 1, "leaky_relu": 2, "swish": 3}
 
@@ -53,6 +55,7 @@ class UnifiedFPN:
         self._weights_ready = False
         self._weight_refs = []      # keeps host/device weight tensors alive until copied
         self._config = None
+        self._scale_buf = None      # e4m3 input scales, a stable device address per engine
 
     def __del__(self):
         h = getattr(self, "_h", None)
@@ -62,13 +65,29 @@ class UnifiedFPN:
 
     # ------------------------------------------------------------------ weights
     def initialize_weights(self, lateral_weights: Sequence[torch.Tensor], lateral_bias: Sequence[torch.Tensor],
-                           output_weights: Sequence[torch.Tensor], output_bias: Sequence[torch.Tensor]) -> None:
+                           output_weights: Sequence[torch.Tensor], output_bias: Sequence[torch.Tensor],
+                           lateral_scales: Sequence[torch.Tensor] | None = None,
+                           output_scales: Sequence[torch.Tensor] | None = None) -> None:
         """Set the neck's fp32 weights (reference: fpn_pytorch.cpp:24-81).
 
         lateral_weights[l]: [256, Cin_l] or [256, Cin_l, 1, 1]; lateral_bias[l]: [256];
         output_weights[l]: [256, 256, 3, 3]; output_bias[l]: [256]; l = 0..3 for P2..P5.
         CPU or CUDA tensors; they are copied (and packed to the compute dtype) here.
+        Weights may also be float8_e4m3fn with per-output-channel ``lateral_scales`` /
+        ``output_scales`` ([256] each, w = q * scale); they are dequantised to fp32 here.
         """
+        def deq(ws, scales):
+            out = []
+            for l, w in enumerate(ws):
+                if w.dtype == E4M3:
+                    if scales is None:
+                        raise ValueError("float8_e4m3fn weights need their per-channel scales")
+                    sc = scales[l].to(device=w.device, dtype=torch.float32).reshape(-1)
+                    w = w.float() * sc.reshape([-1] + [1] * (w.dim() - 1))
+                out.append(w)
+            return out
+        lateral_weights = deq(lateral_weights, lateral_scales)
+        output_weights = deq(output_weights, output_scales)
         for name, seq in (("lateral_weights", lateral_weights), ("lateral_bias", lateral_bias),
                           ("output_weights", output_weights), ("output_bias", output_bias)):
             if len(seq) != 4:
@@ -113,8 +132,8 @@ class UnifiedFPN:
     # ------------------------------------------------------------------ forward
     def _configure(self, feats):
         x0 = feats[0]
-        if x0.dtype not in _DT:
-            raise TypeError("inputs must be float32, float16 or bfloat16")
+        if x0.dtype not in _DT and x0.dtype != E4M3:
+            raise TypeError("inputs must be float32, float16, bfloat16 or float8_e4m3fn")
         for t in feats:
             if not t.is_cuda or t.device != self.device:
                 raise ValueError("All input tensors must be on the engine's CUDA device")
@@ -124,8 +143,8 @@ class UnifiedFPN:
                 raise ValueError("All input tensors must share one dtype")
             if t.shape[0] != x0.shape[0]:
                 raise ValueError("All input tensors must share the batch size")
-        if x0.dtype != torch.float32 and all(
-                t.is_contiguous(memory_format=torch.channels_last) for t in feats):
+        if x0.dtype == E4M3 or (x0.dtype != torch.float32 and all(
+                t.is_contiguous(memory_format=torch.channels_last) for t in feats)):
             layout = _lib.LAYOUT_NHWC
         else:
             layout = _lib.LAYOUT_NCHW
@@ -136,8 +155,9 @@ class UnifiedFPN:
             ci = (ctypes.c_int * 4)(*chans)
             hi = (ctypes.c_int * 4)(*[int(t.shape[2]) for t in feats])
             wi = (ctypes.c_int * 4)(*[int(t.shape[3]) for t in feats])
+            code = _lib.DTYPE_E4M3 if x0.dtype == E4M3 else _DT[x0.dtype]
             check(lib.ufpn_core_configure_levels(self._h, N, ci, hi, wi, self.output_channels,
-                                                 _DT[x0.dtype], layout), "configure_levels")
+                                                 code, layout), "configure_levels")
             self._config = cfg
         if not self._weights_ready or chans != self._channels:
             if self._weights_ready:
@@ -156,18 +176,34 @@ class UnifiedFPN:
 
     def _alloc_outputs(self, feats, mf, return_p6):
         N = feats[0].shape[0]
-        outs = [torch.empty((N, 256, t.shape[2], t.shape[3]), dtype=t.dtype, device=t.device, memory_format=mf)
+        odt = torch.bfloat16 if feats[0].dtype == E4M3 else feats[0].dtype
+        outs = [torch.empty((N, 256, t.shape[2], t.shape[3]), dtype=odt, device=t.device, memory_format=mf)
                 for t in feats]
         p6 = None
         if return_p6:
             H5, W5 = feats[3].shape[2], feats[3].shape[3]
-            p6 = torch.empty((N, 256, (H5 - 1) // 2 + 1, (W5 - 1) // 2 + 1), dtype=feats[0].dtype,
+            p6 = torch.empty((N, 256, (H5 - 1) // 2 + 1, (W5 - 1) // 2 + 1), dtype=odt,
                              device=feats[0].device, memory_format=mf)
         return outs, p6
 
+    def _scale_ptrs(self, input_scales):
+        """Copies the 4 per-tensor input scales into the engine's device buffer (stream
+        ordered, so a captured graph sees the same address every call)."""
+        if input_scales is None or len(input_scales) < 4:
+            raise ValueError("float8_e4m3fn inputs need input_scales for C2..C5")
+        if self._scale_buf is None:
+            self._scale_buf = torch.empty(4, dtype=torch.float32, device=self.device)
+        vals = torch.stack([torch.as_tensor(s, dtype=torch.float32).reshape(()).to(self.device)
+                            for s in input_scales[:4]])
+        self._scale_buf.copy_(vals)
+        base = self._scale_buf.data_ptr()
+        return _ptr_array([base + 4 * l for l in range(4)])
+
     def forward(self, backbone_features: Sequence[torch.Tensor], return_p6: bool = False,
-                out: Sequence[torch.Tensor] | None = None):
-        """P2..P5 (and P6) of the neck; stream-ordered on torch's current stream."""
+                out: Sequence[torch.Tensor] | None = None, input_scales=None):
+        """P2..P5 (and P6) of the neck; stream-ordered on torch's current stream.
+        float8_e4m3fn inputs need ``input_scales`` (4 per-tensor dequantisation scales,
+        floats or 1-element tensors; x = q * scale) and produce bf16 outputs."""
         feats, layout, mf = self._prepare(backbone_features)
         if out is not None:
             outs = list(out[:4])
@@ -178,8 +214,16 @@ class UnifiedFPN:
             outs, p6 = self._alloc_outputs(feats, mf, return_p6)
         ins = _ptr_array([t.data_ptr() for t in feats])
         os_ = _ptr_array([t.data_ptr() for t in outs])
-        check(lib.ufpn_core_forward(self._h, ins, os_, p6.data_ptr() if p6 is not None else None,
-                                    _stream(feats[0])), "forward")
+        if feats[0].dtype == E4M3:
+            sp = self._scale_ptrs(input_scales)
+            check(lib.ufpn_core_forward_e4m3(self._h, ins, sp, os_,
+                                             p6.data_ptr() if p6 is not None else None,
+                                             _stream(feats[0])), "forward")
+        else:
+            if input_scales is not None:
+                raise ValueError("input_scales apply to float8_e4m3fn inputs only")
+            check(lib.ufpn_core_forward(self._h, ins, os_, p6.data_ptr() if p6 is not None else None,
+                                        _stream(feats[0])), "forward")
         return outs + [p6] if return_p6 else outs
 
     __call__ = forward

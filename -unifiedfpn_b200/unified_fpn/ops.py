@@ -174,6 +174,128 @@ def fpn_p6(p5: torch.Tensor) -> torch.Tensor:
     return out
 
 
+# ----------------------------------------------------------------------------- e4m3 (FP8)
+E4M3 = torch.float8_e4m3fn
+
+
+def quantize_fp8(x: torch.Tensor, per_image: bool = False):
+    """Symmetric e4m3 quantisation on the device: returns ``(q, scale)`` with ``q``
+    float8_e4m3fn in ``x``'s memory format and ``scale`` fp32 on the device, one element
+    (per tensor) or one per image along dim 0 (``per_image``); ``x ~ q * scale`` with
+    scale = absmax / 448 and q = e4m3(x * 448 / absmax), rounded to nearest even and
+    saturated."""
+    _check_cuda(x)
+    dt = dtype_code(x)
+    nhwc = x.dim() == 4 and layout_of(x) == _lib.LAYOUT_NHWC
+    mf = torch.channels_last if nhwc else torch.contiguous_format
+    x = x.contiguous(memory_format=mf)
+    groups = int(x.shape[0]) if per_image else 1
+    q = torch.empty_like(x, dtype=E4M3, memory_format=mf)
+    amax = torch.empty(groups, dtype=torch.int32, device=x.device)
+    scale = torch.empty(groups, dtype=torch.float32, device=x.device)
+    check(lib.ufpn_quantize_e4m3(dt, x.data_ptr(), x.numel(), groups, amax.data_ptr(), q.data_ptr(),
+                                 scale.data_ptr(), _stream(x)), "ufpn_quantize_e4m3")
+    return q, scale
+
+
+def quantize_fp8_rows(weight: torch.Tensor, pack3x3: bool = False):
+    """Per-output-channel e4m3 quantisation of fp32 weights: ``(q, scales)``.  Lateral
+    [Cout, Cin] (or [Cout, Cin, 1, 1]) -> q [Cout, Cin]; with ``pack3x3`` a 3x3 kernel
+    [Cout, Cin, 3, 3] -> q [Cout, 9, Cin] (the K order of :func:`fpn_conv3x3_fp8`)."""
+    _check_cuda(weight)
+    Cout = weight.shape[0]
+    w = weight.to(torch.float32).contiguous()
+    cols = w.numel() // Cout
+    if pack3x3:
+        if w.dim() != 4 or w.shape[2:] != (3, 3):
+            raise ValueError("pack3x3 needs a [Cout, Cin, 3, 3] kernel")
+        cin = w.shape[1]
+        q = torch.empty((Cout, 9, cin), dtype=E4M3, device=w.device)
+    else:
+        cin = 0
+        q = torch.empty((Cout, cols), dtype=E4M3, device=w.device)
+    scales = torch.empty(Cout, dtype=torch.float32, device=w.device)
+    check(lib.ufpn_quantize_e4m3_rows(w.data_ptr(), Cout, cols, cin, q.data_ptr(), scales.data_ptr(),
+                                      _stream(w)), "ufpn_quantize_e4m3_rows")
+    return q, scales
+
+
+def _fp8_nhwc(x: torch.Tensor) -> torch.Tensor:
+    if x.dtype != E4M3:
+        raise TypeError("expected a float8_e4m3fn tensor")
+    return x.contiguous(memory_format=torch.channels_last)
+
+
+def _scale_ptr(scale, device, n_images):
+    """(scale tensor, per_image flag): one element = per tensor, n_images = per image."""
+    s = torch.as_tensor(scale, dtype=torch.float32).to(device).reshape(-1).contiguous()
+    if s.numel() == 1:
+        return s, 0
+    if s.numel() == n_images:
+        return s, 1
+    raise ValueError("an activation scale has 1 element (per tensor) or N (per image)")
+
+
+def fpn_lateral_conv_fp8(input: torch.Tensor, input_scale, weight: torch.Tensor,
+                         weight_scales: torch.Tensor, bias: torch.Tensor,
+                         coarse: torch.Tensor | None = None,
+                         amax_out: torch.Tensor | None = None) -> torch.Tensor:
+    """FP8 lateral: ``out = (q_x . q_w^T) * (scale_x * scale_w[o]) + bias[o]
+    [+ bilinear(coarse)]`` on the e4m3 tensor cores, bf16 out (channels_last).
+    ``input`` e4m3 [N, Cin, H, W]; ``weight`` e4m3 [256, Cin] with ``weight_scales`` [256];
+    ``coarse`` bf16 [N, 256, Hc, Wc] or None; ``input_scale`` 1 (per tensor) or N (per
+    image) elements; ``amax_out`` (int32 CUDA [N], optional, zeroed by the caller) receives
+    the per-image atomicMax of |out| as fp32 bits."""
+    _check_cuda(input, weight, weight_scales, bias, coarse, amax_out)
+    x = _fp8_nhwc(input)
+    N, Cin, H, W = x.shape
+    w = weight.reshape(weight.shape[0], -1).contiguous()
+    if w.dtype != E4M3 or w.shape != (256, Cin):
+        raise ValueError("weight must be e4m3 [256, Cin]")
+    ws = weight_scales.to(torch.float32).contiguous()
+    b = bias.to(device=x.device, dtype=torch.float32).contiguous()
+    xs, per_img = _scale_ptr(input_scale, x.device, N)
+    Hc = Wc = 0
+    if coarse is not None:
+        if coarse.dtype != torch.bfloat16 or coarse.shape[:2] != (N, 256):
+            raise ValueError("coarse must be bf16 [N, 256, Hc, Wc]")
+        coarse = coarse.contiguous(memory_format=torch.channels_last)
+        Hc, Wc = coarse.shape[2], coarse.shape[3]
+    out = torch.empty((N, 256, H, W), dtype=torch.bfloat16, device=x.device,
+                      memory_format=torch.channels_last)
+    check(lib.ufpn_lateral_conv_e4m3(x.data_ptr(), xs.data_ptr(), per_img, w.data_ptr(), ws.data_ptr(),
+                                     b.data_ptr(), coarse.data_ptr() if coarse is not None else None,
+                                     out.data_ptr(), N, Cin, H, W, Hc, Wc,
+                                     amax_out.data_ptr() if amax_out is not None else None,
+                                     _stream(x)), "ufpn_lateral_conv_e4m3")
+    return out
+
+
+def fpn_conv3x3_fp8(input: torch.Tensor, input_scale, weight: torch.Tensor,
+                    weight_scales: torch.Tensor, bias: torch.Tensor, p6: bool = False):
+    """FP8 3x3 pad-1 conv 256 -> 256 (+ optional P6): ``input`` e4m3 [N, 256, H, W];
+    ``weight`` e4m3 packed [256, 9, 256] from :func:`quantize_fp8_rows` (pack3x3=True) with
+    ``weight_scales`` [256]; ``input_scale`` 1 (per tensor) or N (per image) elements;
+    bf16 channels_last out."""
+    _check_cuda(input, weight, weight_scales, bias)
+    x = _fp8_nhwc(input)
+    N, C, H, W = x.shape
+    if C != 256 or weight.dtype != E4M3 or tuple(weight.shape) != (256, 9, 256):
+        raise ValueError("expects 256 channels and an e4m3 weight packed [256, 9, 256]")
+    ws = weight_scales.to(torch.float32).contiguous()
+    b = bias.to(device=x.device, dtype=torch.float32).contiguous()
+    xs, per_img = _scale_ptr(input_scale, x.device, N)
+    out = torch.empty((N, 256, H, W), dtype=torch.bfloat16, device=x.device,
+                      memory_format=torch.channels_last)
+    p6t = torch.empty((N, 256, (H - 1) // 2 + 1, (W - 1) // 2 + 1), dtype=torch.bfloat16,
+                      device=x.device, memory_format=torch.channels_last) if p6 else None
+    check(lib.ufpn_conv3x3_e4m3(x.data_ptr(), xs.data_ptr(), per_img, weight.contiguous().data_ptr(),
+                                ws.data_ptr(), b.data_ptr(), out.data_ptr(),
+                                p6t.data_ptr() if p6t is not None else None, N, H, W, None,
+                                _stream(x)), "ufpn_conv3x3_e4m3")
+    return (out, p6t) if p6 else out
+
+
 def device_status(reset: bool = True) -> int:
     """Status word of the standalone tensor-core ops on the current device (0 = ok)."""
     v = _lib.c_int(0)

@@ -11,6 +11,10 @@
 //   * Inputs are C2..C5 (a fifth tensor, C6, is accepted and ignored).
 //   * 16-bit inputs run on the tensor cores (tcgen05 + TMA), fp32 inputs on the
 //     CUDA cores in full fp32.
+//   * FP8_E4M3 inputs (NHWC, each with a per-tensor fp32 scale) run on the fp8
+//     tensor cores: weights are quantised per output channel (absmax / 448) when
+//     set, every merged map M_l is quantised per tensor before its 3x3, and the
+//     outputs P2..P6 are bf16.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -29,7 +33,8 @@ class __attribute__((visibility("default"))) UnifiedFPNCore {
   UnifiedFPNCore& operator=(const UnifiedFPNCore&) = delete;
 
   // backbone_dims: C2..C5 (4 entries) or C2..C6 (5, the last ignored).
-  // dtype: FLOAT32, FLOAT16 or BFLOAT16.  layout: layout of inputs and outputs.
+  // dtype: FLOAT32, FLOAT16, BFLOAT16 or FP8_E4M3 (NHWC only; bf16 outputs).
+  // layout: layout of inputs and outputs.
   void configure_levels(const std::vector<FPNDimensions>& backbone_dims, int output_channels,
                         FPNDataType dtype = FPNDataType::FLOAT32,
                         FPNLayout layout = FPNLayout::NCHW);
@@ -73,6 +78,10 @@ class __attribute__((visibility("default"))) UnifiedFPNCore {
   // Untyped entry point used by the C ABI.
   void forward_raw(const void* const* inputs, void* const* outputs, void* p6,
                    cudaStream_t stream);
+  // FP8_E4M3 inputs: input_scales[l] points to the device fp32 dequantisation scale of
+  // C_{l+2} (x = q * scale).  Other dtypes accept input_scales == nullptr only.
+  void forward_raw_scaled(const void* const* inputs, const float* const* input_scales,
+                          void* const* outputs, void* p6, cudaStream_t stream);
 
   struct Impl;
 

@@ -32,9 +32,27 @@ inline int dtype_size(DType d) {
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // ---- bandwidth kernels (simt_kernels.cu)
+// amax_out (optional): amax_out[n] = atomicMax of |out| of image n as fp32 bits (the caller
+// zeroes them first).
 cudaError_t launch_upsample_add(DType dt, const void* coarse, const void* lat, void* out, int N,
                                 int C, int Hc, int Wc, int H, int W, int align_corners,
-                                Layout layout, cudaStream_t s);
+                                Layout layout, cudaStream_t s, unsigned* amax_out = nullptr);
+// ---- e4m3 quantisation (simt_kernels.cu).  scale = amax / 448, q = e4m3_rn_satfinite(
+// x * (448 / amax)) (amax == 0: scale = 1, q = 0); amax carried as fp32 bits.
+// The n elements form `groups` equal consecutive groups (images), each with its own
+// absmax amax_bits[g] and scale scale_out[g].
+// atomicMax of max|x| of each group into amax_bits[g] (the caller zeroes them first).
+cudaError_t launch_absmax(DType dt, const void* x, long long n, int groups, unsigned* amax_bits,
+                          cudaStream_t s);
+// Quantisation with the absmax values in amax_bits[groups]; writes the dequantisation
+// scales to scale_out[groups] (device, may be null).
+cudaError_t launch_quantize_e4m3(DType dt, const void* x, long long n, int groups,
+                                 const unsigned* amax_bits, void* q, float* scale_out,
+                                 cudaStream_t s);
+// Per-row (output channel) quantisation of fp32 weights [rows][cols] -> e4m3 + scales[rows].
+// pack_cin > 0: rows are [pack_cin][3][3] and q is written [9][pack_cin] (3x3 K order).
+cudaError_t launch_quantize_rows_e4m3(const float* w, int rows, int cols, int pack_cin, void* q,
+                                      float* scales, cudaStream_t s);
 cudaError_t launch_p6(DType dt, const void* in, void* out, int N, int C, int H, int W,
                       Layout layout, cudaStream_t s);
 cudaError_t launch_transpose(DType dt, const void* in, void* out, int N, int C, int HW,
@@ -82,18 +100,30 @@ struct TcPlan {
   int num_tiles = 0;
 };
 
+// Device-resident scale operands of one tensor-core launch.  dtype E4M3 (x and w e4m3,
+// coarse / out / p6 bf16): out = acc * (ascale[n or 0] * wscale[o]) + bias[o]; both
+// required.  amax_out (any dtype, optional): amax_out[n] = atomicMax of |stored output| of
+// image n as fp32 bits, for a following per-image e4m3 quantisation of the output.
+struct TcScales {
+  const float* ascale = nullptr;  // activation scale(s) (device)
+  bool ascale_per_image = false;  // ascale[n] per image, else ascale[0] for the tensor
+  const float* wscale = nullptr;  // per-output-channel weight scales [256], 16-byte aligned
+  unsigned* amax_out = nullptr;   // [N] (device), zeroed by the caller
+};
+
 // Lateral 1x1 (+ optional fused bilinear upsample-add of the coarser merged map).
 //   x: NHWC [N][H][W][Cin]; w: [256][Cin] (dtype, K-major); bias fp32 [256];
 //   coarse: NHWC [N][Hc][Wc][256] or null; out: NHWC [N][H][W][256].
 cudaError_t plan_tc_lateral(TcPlan& plan, DType dt, const void* x, const void* w,
                             const float* bias, const void* coarse, void* out, int N, int Cin,
                             int H, int W, int Hc, int Wc, Conv3x3Tiling tiling, int* status,
-                            int max_ctas);
+                            int max_ctas, const TcScales& scales = TcScales());
 // 3x3 pad-1 conv, 256 -> 256: x NHWC [N][H][W][256]; w: [256][9][256]; out NHWC;
-// p6 (optional) NHWC [N][ceil(H/2)][ceil(W/2)][256].
+// p6 (optional) NHWC [N][ceil(H/2)][ceil(W/2)][256].  E4M3 requires the halo tiling.
 cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w,
                             const float* bias, void* out, void* p6, int N, int H, int W,
-                            Conv3x3Tiling tiling, int* status, int max_ctas);
+                            Conv3x3Tiling tiling, int* status, int max_ctas,
+                            const TcScales& scales = TcScales());
 // Tiling with the fewest padded pixels for an H x W map (ties: 16 wide).
 Conv3x3Tiling default_tiling(int H, int W);
 

@@ -168,6 +168,54 @@ int ufpn_convert_weights(int dtype, const float* w, void* out, long long count, 
 int ufpn_layout_convert(int dtype, const void* in, void* out, int N, int C, int H, int W,
                         int to_nhwc, void* stream);
 
+/* ---------------------------------------------------------------- e4m3 (FP8) path
+ * The reference declares FPNDataType::FP8_E4M3 (include/unified_fpn/core/types.h:208-223)
+ * but never computes in it; these entry points are the FP8 neck of the same ops.
+ * Quantisation is symmetric with scale = absmax / 448:
+ *   amax > 0: q = e4m3_rn_satfinite(x * (448 / amax)), scale = amax / 448
+ *   amax = 0: q = 0, scale = 1
+ * each step a single correctly rounded fp32 operation; x ~ q * scale.
+ * Absmax values travel as the bit pattern of a non-negative fp32 in an unsigned word. */
+
+/* The count elements form `groups` equal consecutive groups (e.g. images), each with its
+ * own absmax and scale.  atomicMax of max|x| of group g (dtype F32/F16/BF16) into
+ * amax_bits[g] (device; zero them first). */
+int ufpn_absmax(int dtype, const void* x, long long count, int groups, unsigned* amax_bits,
+                void* stream);
+/* Quantisation of x (dtype F32/F16/BF16, count elements in `groups` equal groups) to e4m3 q
+ * (count bytes).  amax_ws: device unsigned scratch [groups]; scale_out: device fp32
+ * [groups], the dequantisation scales. */
+int ufpn_quantize_e4m3(int dtype, const void* x, long long count, int groups, unsigned* amax_ws,
+                       void* q, float* scale_out, void* stream);
+/* Per-row (output channel) quantisation of fp32 weights [rows][cols] to e4m3 + scales[rows].
+ * pack_cin > 0: each row is [pack_cin][3][3] (cols = 9 * pack_cin) and is written tap-major
+ * [9][pack_cin], the K order of ufpn_conv3x3_e4m3; pack_cin = 0: lateral [rows][cols]. */
+int ufpn_quantize_e4m3_rows(const float* w, int rows, int cols, int pack_cin, void* q,
+                            float* scales, void* stream);
+/* FP8 lateral 1x1 (+ optional top-down add), NHWC: x e4m3 [N][H][W][Cin] with device scale(s)
+ * x_scale[0] (x_scale_per_image = 0) or x_scale[n]; w e4m3 [256][Cin] with scales [256];
+ * coarse bf16 [N][Hc][Wc][256] or NULL; out bf16 = acc * (x_scale * w_scales[o]) + bias[o]
+ * (+ bilinear(coarse)).  amax_out (device [N], may be NULL): per-image atomicMax of |out|.
+ * Same roles as launch_lateral_conv / lateral_conv_kernel (fpn_engine.cu:248-272). */
+int ufpn_lateral_conv_e4m3(const void* x, const float* x_scale, int x_scale_per_image,
+                           const void* w, const float* w_scales, const float* bias,
+                           const void* coarse, void* out, int N, int Cin, int H, int W, int Hc,
+                           int Wc, unsigned* amax_out, void* stream);
+/* FP8 3x3 pad-1 conv 256 -> 256 (8 x 16 halo tiles), NHWC: x e4m3 [N][H][W][256] with device
+ * scale(s) as above; w e4m3 packed [256][9][256] (ufpn_quantize_e4m3_rows with pack_cin =
+ * 256) with scales [256]; out (and optional p6 = out[::2, ::2]) bf16; amax_out as above.
+ * Same role as launch_output_conv (fpn_engine.cu:315-362). */
+int ufpn_conv3x3_e4m3(const void* x, const float* x_scale, int x_scale_per_image, const void* w,
+                      const float* w_scales, const float* bias, void* out, void* p6, int N,
+                      int H, int W, unsigned* amax_out, void* stream);
+/* fpn_engine.cu:191-245 (forward) for an engine configured with dtype UFPN_DTYPE_E4M3
+ * (NHWC): inputs C2..C5 e4m3, input_scales[l] = device fp32 per-tensor scale of inputs[l];
+ * outputs P2..P5 (and p6) bf16.  Each merged map M_l is quantised per image before its 3x3,
+ * so an image's outputs do not depend on the rest of the batch. */
+int ufpn_core_forward_e4m3(ufpn_core* core, const void* const* inputs,
+                           const float* const* input_scales, void* const* outputs, void* p6,
+                           void* stream);
+
 /* ---------------------------------------------------------------- reference C ABI
  * Same names and argument meaning as the reference's exported functions.  NHWC
  * tensors (the layout of the reference's kernels).  These time the launch with

@@ -22,6 +22,10 @@ What it restates (paths relative to the sanowl/-UnifiedFPN source tree):
   (full 256->256, pad 1, bias); P6 = max_pool2d(P5, 1, 2).  The 3x3 conv and
   max-pool use torch's CPU kernels (the reference has no CPU version of them;
   its device kernel is a depthwise 3x3, fpn_compute_kernels.cu:277-340).
+* ``fpn_neck_e4m3`` -- the same neck with e4m3 inputs/weights (per-tensor and
+  per-output-channel scales = absmax / 448), quantising each merged map before its
+  3x3 and storing bf16 where the CUDA schedule does; ``e4m3_round`` is the
+  nearest-even e4m3fn rounding, pinned against torch's float8_e4m3fn conversion.
 
 Tolerances (fp32 <= 1e-4, bf16/fp16 <= 1e-2, FP8 <= 3e-2) are relative to the
 largest magnitude of the reference output: ``rel_err(y, ref) = max|y - ref| / max|ref|``.
@@ -165,23 +169,130 @@ def config1_inputs(seed=0):
 
 
 # ----------------------------------------------------------------------------- FP8 (e4m3)
+# The reference declares FPNDataType::FP8_E4M3 (include/unified_fpn/core/types.h:208-223)
+# but has no FP8 arithmetic; the FP8 neck follows the quantisation the benchmark
+# configuration states (e4m3 weights with per-output-channel scale = absmax / 448,
+# activations e4m3 with a per-tensor scale = absmax / 448, fp32 accumulate, bf16 out),
+# made exact so the CUDA path can be checked element by element:
+#   amax > 0: inv = fp32(448 / amax), scale = fp32(amax / 448); amax == 0: inv = scale = 1
+#   q = e4m3(fp32(x * inv)), round to nearest even, saturate to +-448
 E4M3_MAX = 448.0
 
 
+def e4m3_round(v: np.ndarray) -> np.ndarray:
+    """Nearest-even rounding of fp32 values onto the e4m3fn grid (saturating at +-448):
+    normals 2^-6 <= |v| have 3 fraction bits, below that the grid step is 2^-9."""
+    v = np.asarray(v, dtype=np.float64)
+    a = np.abs(v)
+    _, ex = np.frexp(a)                      # a = m * 2^ex, m in [0.5, 1)
+    step = np.ldexp(1.0, np.maximum(ex - 4, -9))
+    q = np.rint(a / step) * step             # rint: ties to even
+    q = np.minimum(q, E4M3_MAX)
+    return (np.sign(v) * q).astype(np.float32)
+
+
+def _e4m3_inv_scale(amax: np.float32):
+    if amax > 0:
+        return np.float32(np.float32(448.0) / amax), np.float32(amax / np.float32(448.0))
+    return np.float32(1.0), np.float32(1.0)
+
+
+def quantize_e4m3_tensor(x):
+    """Per-tensor quantisation: returns (codes as fp32 values, scale as np.float32)."""
+    x = np.asarray(torch.as_tensor(x).float().numpy(), dtype=np.float32)
+    amax = np.float32(np.abs(x).max()) if x.size else np.float32(0)
+    inv, scale = _e4m3_inv_scale(amax)
+    return e4m3_round((x * inv).astype(np.float32)), scale
+
+
+def quantize_e4m3_images(x):
+    """Per-image (dim 0) quantisation: (codes fp32 like x, scales [N] fp32)."""
+    x = torch.as_tensor(x).float()
+    qs, ss = zip(*[quantize_e4m3_tensor(x[n]) for n in range(x.shape[0])])
+    return np.stack(qs), np.array(ss, dtype=np.float32)
+
+
+def quantize_e4m3_rows(w):
+    """Per-output-channel (dim 0) quantisation: (codes [rows, ...] fp32, scales [rows] fp32)."""
+    w = np.asarray(torch.as_tensor(w).float().numpy(), dtype=np.float32)
+    rows = w.reshape(w.shape[0], -1)
+    q = np.empty_like(rows)
+    scales = np.empty(rows.shape[0], dtype=np.float32)
+    for r in range(rows.shape[0]):
+        amax = np.float32(np.abs(rows[r]).max())
+        inv, scales[r] = _e4m3_inv_scale(amax)
+        q[r] = e4m3_round((rows[r] * inv).astype(np.float32))
+    return q.reshape(w.shape), scales
+
+
 def quantize_e4m3(x: torch.Tensor, per_channel_dim: int | None = None):
-    """Symmetric e4m3 quantisation with scale = absmax / 448 (per tensor, or per
-    slice along ``per_channel_dim``).  Returns (dequantised fp32 tensor, scale)."""
-    x = x.float()
+    """Dequantised fp32 tensor and scale(s) of the quantisation above (per tensor, or per
+    output channel for ``per_channel_dim=0``)."""
     if per_channel_dim is None:
-        amax = x.abs().max().clamp_min(1e-12)
-        scale = amax / E4M3_MAX
-        q = (x / scale).to(torch.float8_e4m3fn)
-        return q.float() * scale, scale
-    dims = [d for d in range(x.dim()) if d != per_channel_dim]
-    amax = x.abs().amax(dim=dims, keepdim=True).clamp_min(1e-12)
-    scale = amax / E4M3_MAX
-    q = (x / scale).to(torch.float8_e4m3fn)
-    return q.float() * scale, scale
+        q, s = quantize_e4m3_tensor(x)
+        return torch.from_numpy(q * s), torch.tensor(s)
+    if per_channel_dim != 0:
+        raise ValueError("per-channel quantisation is along dim 0 (output channels)")
+    q, s = quantize_e4m3_rows(x)
+    shape = [-1] + [1] * (q.ndim - 1)
+    return torch.from_numpy(q * s.reshape(shape)), torch.from_numpy(s).reshape(shape)
+
+
+@dataclass
+class NeckWeightsE4M3:
+    lat_q: list   # e4m3 codes [256, Cin] (fp32 values)
+    lat_s: list   # [256] fp32
+    lat_b: list
+    out_q: list   # e4m3 codes [256, 256, 3, 3]
+    out_s: list
+    out_b: list
+
+
+def quantize_neck_weights(wts: NeckWeights) -> NeckWeightsE4M3:
+    lq, ls, oq, os_ = [], [], [], []
+    for l in range(4):
+        q, sc = quantize_e4m3_rows(wts.lat_w[l])
+        lq.append(torch.from_numpy(q))
+        ls.append(torch.from_numpy(sc))
+        q, sc = quantize_e4m3_rows(wts.out_w[l])
+        oq.append(torch.from_numpy(q))
+        os_.append(torch.from_numpy(sc))
+    return NeckWeightsE4M3(lq, ls, [b.float() for b in wts.lat_b], oq, os_, [b.float() for b in wts.out_b])
+
+
+def _bf16(x: torch.Tensor) -> torch.Tensor:
+    return x.to(torch.bfloat16).float()
+
+
+def fpn_neck_e4m3(q_feats, in_scales, qw: NeckWeightsE4M3, return_merged: bool = False):
+    """FP8 neck with the storage points of the CUDA schedule: e4m3 inputs C_l = q_l * s_l;
+    laterals in fp64 from the codes, scaled by s_l * w_scale[o] (+ bias) and stored bf16;
+    M_l = bf16(L_l + up(M_{l+1})) (P2: one rounding of L_2 + up(M_3)); each M_l quantised
+    per image to e4m3 before its 3x3; P_l = bf16(3x3 of the dequantised codes + bias);
+    P6 = P5[::2, ::2].  Returns [P2, P3, P4, P5, P6] as fp32 tensors (bf16 values)."""
+    merged = [None] * 4
+    for l in (3, 2, 1, 0):
+        x = q_feats[l].double()
+        acc = F.conv2d(x, qw.lat_q[l].double().reshape(256, -1, 1, 1))
+        cs = (torch.tensor(np.float32(in_scales[l])).float() * qw.lat_s[l]).double()  # fp32 product
+        m = acc * cs.reshape(1, -1, 1, 1) + qw.lat_b[l].double().reshape(1, -1, 1, 1)
+        if l == 0:
+            m = _bf16((m + bilinear_upsample_t(merged[1].double(), m.shape[-2:])).float())
+        elif l < 3:
+            m = _bf16((_bf16(m.float()).double() + bilinear_upsample_t(merged[l + 1].double(),
+                                                                        m.shape[-2:])).float())
+        else:
+            m = _bf16(m.float())
+        merged[l] = m
+    outs = []
+    for l in range(4):
+        q, s = quantize_e4m3_images(merged[l])
+        acc = F.conv2d(torch.from_numpy(q).double(), qw.out_q[l].double(), padding=1)
+        cs = (torch.from_numpy(s).reshape(-1, 1) * qw.out_s[l].reshape(1, -1)).double()  # fp32
+        outs.append(_bf16((acc * cs.reshape(cs.shape[0], -1, 1, 1)
+                           + qw.out_b[l].double().reshape(1, -1, 1, 1)).float()))
+    outs.append(p6_maxpool(outs[3]))
+    return (outs, merged) if return_merged else outs
 
 
 # ----------------------------------------------------------------------------- checking

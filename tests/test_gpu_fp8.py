@@ -1,0 +1,229 @@
+"""GPU parity tests of the FP8 (e4m3) path against the CPU oracle: quantisers bit for bit,
+the e4m3 lateral and 3x3 kernels, and the whole FP8 neck (UnifiedFPN with
+float8_e4m3fn inputs) including the FP8 benchmark's per-GPU shape."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import fpn_oracle as O
+
+pytestmark = pytest.mark.gpu
+TOL8 = O.TOL["e4m3"]   # 3e-2, max-norm relative
+E4M3 = torch.float8_e4m3fn
+
+
+def _cl(x):
+    return x.contiguous(memory_format=torch.channels_last)
+
+
+def _codes(q: torch.Tensor) -> np.ndarray:
+    """e4m3 tensor (any layout) -> its values as fp32 numpy in logical NCHW order."""
+    return q.float().cpu().numpy()
+
+
+def _upload_codes(codes, device="cuda"):
+    return torch.from_numpy(np.ascontiguousarray(codes)).to(E4M3).to(device)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("shape", [(2, 64, 9, 13), (3, 1001)])
+def test_quantize_fp8_bitexact(cuda_device, dtype, shape):
+    import unified_fpn as U
+    g = torch.Generator().manual_seed(11)
+    x = (torch.randn(*shape, generator=g) * 3).to(dtype)
+    xd = x.cuda()
+    if xd.dim() == 4:
+        xd = _cl(xd)
+    q, s = U.quantize_fp8(xd)
+    qo, so = O.quantize_e4m3_tensor(x.float())
+    np.testing.assert_array_equal(_codes(q), qo)
+    assert s.item() == float(so)
+    # per-image groups
+    q2, s2 = U.quantize_fp8(xd, per_image=True)
+    qo2, so2 = O.quantize_e4m3_images(x.float())
+    np.testing.assert_array_equal(_codes(q2), qo2)
+    np.testing.assert_array_equal(s2.cpu().numpy(), so2)
+
+
+def test_quantize_fp8_zero_tensor(cuda_device):
+    import unified_fpn as U
+    q, s = U.quantize_fp8(torch.zeros(4, 64, device="cuda", dtype=torch.bfloat16))
+    assert s.item() == 1.0 and not q.float().any()
+
+
+def test_quantize_fp8_rows_bitexact(cuda_device):
+    import unified_fpn as U
+    g = torch.Generator().manual_seed(12)
+    wl = torch.randn(256, 512, generator=g) * 0.06
+    w3 = torch.randn(256, 256, 3, 3, generator=g) * 0.03
+    ql, sl = U.quantize_fp8_rows(wl.cuda())
+    qo, so = O.quantize_e4m3_rows(wl)
+    np.testing.assert_array_equal(_codes(ql), qo)
+    np.testing.assert_array_equal(sl.cpu().numpy(), so)
+    q3, s3 = U.quantize_fp8_rows(w3.cuda(), pack3x3=True)
+    qo3, so3 = O.quantize_e4m3_rows(w3)
+    packed = qo3.reshape(256, 256, 9).transpose(0, 2, 1)        # [o][tap][c]
+    np.testing.assert_array_equal(_codes(q3), packed)
+    np.testing.assert_array_equal(s3.cpu().numpy(), so3)
+
+
+def _lateral_oracle(qx, sx, qw, sw, b, coarse=None):
+    acc = torch.nn.functional.conv2d(torch.from_numpy(qx).double(),
+                                     torch.from_numpy(qw).double().reshape(256, -1, 1, 1))
+    sx = np.asarray(sx, dtype=np.float32).reshape(-1)
+    cs = (torch.from_numpy(sx).reshape(-1, 1) * torch.from_numpy(sw).reshape(1, -1)).double()
+    y = acc * cs.reshape(cs.shape[0], -1, 1, 1) + b.double().reshape(1, -1, 1, 1)
+    if coarse is not None:
+        y = y + O.bilinear_upsample_t(coarse.double(), y.shape[-2:])
+    return y.float().to(torch.bfloat16).float()
+
+
+@pytest.mark.parametrize("geom", [
+    (2, 512, (40, 56), None),
+    (2, 256, (50, 76), (25, 38)),      # 2x top-down
+    (1, 128, (100, 167), (50, 84)),    # Swin odd, non-2x
+    (1, 2048, (20, 20), None),
+])
+def test_lateral_fp8_matches_oracle(cuda_device, geom):
+    import unified_fpn as U
+    N, Cin, (H, W), csz = geom
+    g = torch.Generator().manual_seed(13)
+    x = torch.randn(N, Cin, H, W, generator=g)
+    w = torch.randn(256, Cin, generator=g) * (2.0 / Cin) ** 0.5
+    b = (torch.rand(256, generator=g) * 2 - 1) * 0.1
+    qx, sx = O.quantize_e4m3_tensor(x)
+    qw, sw = O.quantize_e4m3_rows(w)
+    coarse = None if csz is None else torch.randn(N, 256, *csz, generator=g).to(torch.bfloat16).float()
+    amax = torch.zeros(N, dtype=torch.int32, device="cuda")
+    out = U.fpn_lateral_conv_fp8(_cl(_upload_codes(qx)), torch.tensor([float(sx)]),
+                                 _upload_codes(qw), torch.from_numpy(sw).cuda(), b.cuda(),
+                                 None if coarse is None else _cl(coarse.to(torch.bfloat16).cuda()),
+                                 amax_out=amax)
+    torch.cuda.synchronize()
+    assert U.device_status() == 0
+    ref = _lateral_oracle(qx, sx, qw, sw, b, coarse)
+    assert O.rel_err(out.float().cpu(), ref) < 1e-2
+    # per-image absmax of the stored bf16 output, bit for bit
+    per_img = out.float().abs().amax(dim=(1, 2, 3)).cpu()
+    got = amax.cpu().view(torch.float32)
+    assert torch.equal(got, per_img)
+
+
+@pytest.mark.parametrize("per_image", [False, True])
+@pytest.mark.parametrize("shape", [(2, 40, 56), (1, 25, 38), (3, 13, 21)])
+def test_conv3x3_fp8_matches_oracle(cuda_device, shape, per_image):
+    import unified_fpn as U
+    N, H, W = shape
+    g = torch.Generator().manual_seed(14)
+    m = torch.randn(N, 256, H, W, generator=g)
+    w3 = torch.randn(256, 256, 3, 3, generator=g) * (2.0 / 2304) ** 0.5
+    b = (torch.rand(256, generator=g) * 2 - 1) * 0.1
+    if per_image:
+        qm, sm = O.quantize_e4m3_images(m)
+    else:
+        qm, s1 = O.quantize_e4m3_tensor(m)
+        sm = np.array([s1], dtype=np.float32)
+    qw, sw = O.quantize_e4m3_rows(w3)
+    qwd, swd = U.quantize_fp8_rows(w3.cuda(), pack3x3=True)
+    out, p6 = U.fpn_conv3x3_fp8(_cl(_upload_codes(qm)), torch.from_numpy(sm), qwd, swd, b.cuda(),
+                                p6=True)
+    torch.cuda.synchronize()
+    assert U.device_status() == 0
+    acc = torch.nn.functional.conv2d(torch.from_numpy(qm).double(), torch.from_numpy(qw).double(),
+                                     padding=1)
+    cs = (torch.from_numpy(sm).reshape(-1, 1) * torch.from_numpy(sw).reshape(1, -1)).double()
+    ref = (acc * cs.reshape(cs.shape[0], -1, 1, 1) + b.double().reshape(1, -1, 1, 1)).float()
+    ref = ref.to(torch.bfloat16).float()
+    assert O.rel_err(out.float().cpu(), ref) < 1e-2
+    assert torch.equal(p6.cpu(), out[:, :, ::2, ::2].cpu())
+
+
+def _fp8_case(batch, chans, sizes, seed, bias_scale=0.1):
+    feats = O.make_features(batch, chans, sizes, seed=seed, dist="normal")
+    wts = O.make_weights(chans, seed=seed + 1, bias_scale=bias_scale)
+    qf, sc = zip(*[O.quantize_e4m3_tensor(f) for f in feats])
+    return feats, wts, [torch.from_numpy(q) for q in qf], list(sc)
+
+
+def _run_fp8_neck(chans, wts, qf, sc, fpn=None):
+    import unified_fpn as U
+    fpn = fpn or U.UnifiedFPN()
+    fpn.initialize_weights(wts.lat_w, wts.lat_b, wts.out_w, wts.out_b)
+    xin = [_cl(q.to(E4M3).cuda()) for q in qf]
+    outs = fpn(xin, return_p6=True, input_scales=[float(s) for s in sc])
+    torch.cuda.synchronize()
+    assert fpn.device_status() == 0
+    return fpn, xin, outs
+
+
+@pytest.mark.parametrize("geom", [
+    (2, O.R50_CHANNELS, O.level_sizes(128, 192)),
+    (1, O.SWIN_CHANNELS, [(100, 167), (50, 84), (25, 42), (13, 21)]),
+    (2, O.R50_CHANNELS, O.level_sizes(640, 640)),   # the FP8 benchmark's image size
+])
+def test_fp8_neck_matches_oracle(cuda_device, geom):
+    batch, chans, sizes = geom
+    feats, wts, qf, sc = _fp8_case(batch, chans, sizes, seed=21)
+    fpn, _, outs = _run_fp8_neck(chans, wts, qf, sc)
+    ref = O.fpn_neck_e4m3(qf, sc, O.quantize_neck_weights(wts))
+    for o, r in zip(outs, ref):
+        assert o.dtype == torch.bfloat16 and tuple(o.shape) == tuple(r.shape)
+        assert o.is_contiguous(memory_format=torch.channels_last)
+        err = O.rel_err(o.float().cpu(), r)
+        assert err < TOL8, err
+    # accuracy against the unquantised fp32 neck, reported by the assertion message only
+    full = O.fpn_neck(feats, wts)
+    drift = [round(O.rel_err(o.float().cpu(), r), 4) for o, r in zip(outs, full)]
+    assert max(drift) < 0.15, drift
+
+
+def test_fp8_neck_batch_sharding_is_exact(cuda_device):
+    """M_l is quantised per image, so each image's outputs are independent of the rest of
+    the batch: a batch slice (one GPU's shard) gives bit-identical results."""
+    chans, sizes = O.R50_CHANNELS, O.level_sizes(160, 224)
+    _, wts, qf, sc = _fp8_case(4, chans, sizes, seed=31)
+    fpn, xin, full = _run_fp8_neck(chans, wts, qf, sc)
+    for lo, hi in ((0, 1), (1, 3), (3, 4)):
+        part = fpn([_cl(x[lo:hi]) for x in xin], return_p6=True, input_scales=[float(s) for s in sc])
+        torch.cuda.synchronize()
+        for a, b in zip(full, part):
+            assert torch.equal(a[lo:hi], b)
+
+
+def test_fp8_neck_benchmark_shard_full_size(cuda_device):
+    """One GPU's shard of the FP8 benchmark at full size: R50 neck, 16 images at 640x640,
+    e4m3 inputs.  Size-independent properties: graph replay == direct launch bitwise,
+    repeat determinism, and image 0 equals the oracle on that image alone."""
+    import unified_fpn as U
+    chans, sizes = O.R50_CHANNELS, O.level_sizes(640, 640)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    feats = [torch.randn(16, c, h, w, generator=g, device="cuda") for c, (h, w) in zip(chans, sizes)]
+    qs = [U.quantize_fp8(_cl(f)) for f in feats]
+    xin = [q for q, _ in qs]
+    scales = [s for _, s in qs]
+    wts = O.make_weights(chans, seed=6)
+    fpn = U.UnifiedFPN()
+    fpn.initialize_weights(wts.lat_w, wts.lat_b, wts.out_w, wts.out_b)
+    outs = fpn(xin, return_p6=True, input_scales=scales)
+    again = fpn(xin, return_p6=True, input_scales=scales)
+    fpn.set_kernel_config(enable_graph_capture=False)
+    direct = fpn(xin, return_p6=True, input_scales=scales)
+    torch.cuda.synchronize()
+    assert fpn.device_status() == 0
+    for a, b, c in zip(outs, again, direct):
+        assert torch.equal(a, b) and torch.equal(a, c)
+    qf0 = [torch.from_numpy(_codes(x[:1])) for x in xin]
+    ref = O.fpn_neck_e4m3(qf0, [np.float32(s.item()) for s in scales], O.quantize_neck_weights(wts))
+    for o, r in zip(outs, ref):
+        assert O.rel_err(o[:1].float().cpu(), r) < TOL8
+
+
+def test_fp8_errors(cuda_device):
+    import unified_fpn as U
+    fpn = U.UnifiedFPN()
+    x = [_cl(torch.zeros(1, c, 8, 8, device="cuda").to(E4M3)) for c in O.R50_CHANNELS]
+    with pytest.raises(ValueError):
+        fpn(x)                                  # no input scales
+    with pytest.raises(ValueError):
+        fpn([torch.zeros(1, c, 8, 8, device="cuda", dtype=torch.bfloat16) for c in O.R50_CHANNELS],
+            input_scales=[1.0] * 4)             # scales for a 16-bit neck

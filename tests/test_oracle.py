@@ -140,5 +140,62 @@ def test_fp8_quantiser_roundtrip_error_bounded():
     assert O.rel_err(dq2, x) < 0.07
 
 
+def _e4m3_grid():
+    """Every finite non-negative e4m3fn value, from torch's own float8 type."""
+    codes = torch.arange(0, 0x7F, dtype=torch.uint8)  # 0x7F is NaN
+    return codes.view(torch.float8_e4m3fn).float().numpy()
+
+
+def test_e4m3_round_pinned_to_torch_float8():
+    """The oracle's nearest-even e4m3 rounding equals torch's float8_e4m3fn conversion on
+    random values, on every grid point, on every midpoint between neighbours (ties to even),
+    across the subnormal range, and saturates at 448."""
+    g = torch.Generator().manual_seed(5)
+    grid = _e4m3_grid()
+    mids = ((grid[1:].astype(np.float64) + grid[:-1]) / 2).astype(np.float32)
+    vals = np.concatenate([
+        (torch.randn(200000, generator=g) * 40).numpy().clip(-448, 448),
+        (torch.rand(50000, generator=g) * 2 ** -5 - 2 ** -6).numpy(),
+        grid, -grid, mids, -mids]).astype(np.float32)
+    ref = torch.from_numpy(vals).to(torch.float8_e4m3fn).float().numpy()
+    np.testing.assert_array_equal(O.e4m3_round(vals), ref)
+    assert O.e4m3_round(np.array([460.0, -1e6], dtype=np.float32)).tolist() == [448.0, -448.0]
+
+
+def test_e4m3_tensor_quantisation_definition():
+    x = torch.randn(3, 7, 11, generator=torch.Generator().manual_seed(2))
+    q, s = O.quantize_e4m3_tensor(x)
+    amax = np.float32(x.abs().max().item())
+    assert s == np.float32(amax / np.float32(448))
+    assert np.abs(q).max() == 448.0                      # the absmax element maps to 448
+    inv = np.float32(np.float32(448) / amax)
+    np.testing.assert_array_equal(q, O.e4m3_round((x.numpy() * inv).astype(np.float32)))
+    qz, sz = O.quantize_e4m3_tensor(torch.zeros(5))
+    assert sz == 1.0 and not qz.any()
+    qr, sr = O.quantize_e4m3_rows(torch.randn(4, 9))
+    assert sr.shape == (4,) and (np.abs(qr).max(axis=1) == 448.0).all()
+
+
+def test_fp8_neck_accuracy_vs_fp32():
+    """FP8 neck (e4m3 inputs, weights and merged maps) against the fp32 neck run on the
+    dequantised e4m3 inputs and weights: relative L2 error within the FP8 tolerance.
+    (Max-norm error is reported alongside: ~2.5-3% from e4m3's 3-bit mantissa on M_l.)"""
+    chans, sizes = O.R50_CHANNELS, O.level_sizes(96, 128)
+    feats = O.make_features(1, chans, sizes, seed=7, dist="normal")
+    wts = O.make_weights(chans, seed=8, bias_scale=0.1)
+    qf, sc = zip(*[O.quantize_e4m3_tensor(f) for f in feats])
+    qf = [torch.from_numpy(q) for q in qf]
+    qw = O.quantize_neck_weights(wts)
+    outs = O.fpn_neck_e4m3(qf, sc, qw)
+    dq = [q * s for q, s in zip(qf, sc)]
+    dw = O.NeckWeights([q * s.reshape(-1, 1) for q, s in zip(qw.lat_q, qw.lat_s)], wts.lat_b,
+                       [q * s.reshape(-1, 1, 1, 1) for q, s in zip(qw.out_q, qw.out_s)], wts.out_b)
+    ref = O.fpn_neck(dq, dw)
+    for y, r in zip(outs, ref):
+        l2 = ((y - r).norm() / r.norm()).item()
+        assert l2 < O.TOL["e4m3"], l2
+        assert O.rel_err(y, r) < 0.05
+
+
 def test_level_sizes_r50_800x1216():
     assert O.level_sizes(800, 1216) == [(200, 304), (100, 152), (50, 76), (25, 38)]
