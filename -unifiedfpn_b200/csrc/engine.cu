@@ -98,7 +98,8 @@ struct UnifiedFPNCore::Impl {
   float* out_ws[4] = {};
   DType packed_dtype = DType::F32;
   void* merged[4] = {};   // M_l in the compute dtype (bf16 for e4m3 inputs)
-  void* qmerged[4] = {};  // e4m3: M_l quantised per tensor (input of the 3x3)
+  void* qmerged[4] = {};  // e4m3: M_l quantised per image (input of the 3x3)
+  void* m3_scaled = nullptr;  // e4m3: M3 / (scale(C2) * lateral-P2 weight scale), per channel
   const float* in_scale[4] = {};  // e4m3: scales of the current forward's inputs
   unsigned* fp8_amax = nullptr;   // e4m3: [4][N] per-image absmax of M_l (fp32 bits)
   float* fp8_scale = nullptr;     // e4m3: [4][N] per-image dequantisation scale of M_l
@@ -112,6 +113,8 @@ struct UnifiedFPNCore::Impl {
   bool trace_next = false;
   unsigned long long last_trace[8] = {};
   cudaStream_t side = nullptr;
+  cudaStream_t lat_side[2] = {};  // e4m3: the P4 and P3 laterals beside the P5 one
+  cudaEvent_t ev_lat_done[2] = {};
   cudaStream_t capture = nullptr;
   cudaStream_t setup = nullptr;
   cudaEvent_t ev_fork = nullptr;
@@ -154,6 +157,8 @@ struct UnifiedFPNCore::Impl {
     cudaFree(fp8_amax);  // one allocation with fp8_scale
     fp8_amax = nullptr;
     fp8_scale = nullptr;
+    cudaFree(m3_scaled);
+    m3_scaled = nullptr;
     workspace_bytes = 0;
   }
   void free_weights() {
@@ -185,6 +190,12 @@ struct UnifiedFPNCore::Impl {
     if (capture) cudaStreamDestroy(capture);
     if (setup) cudaStreamDestroy(setup);
     side = capture = setup = nullptr;
+    for (int i = 0; i < 2; ++i) {
+      if (lat_side[i]) cudaStreamDestroy(lat_side[i]);
+      if (ev_lat_done[i]) cudaEventDestroy(ev_lat_done[i]);
+      lat_side[i] = nullptr;
+      ev_lat_done[i] = nullptr;
+    }
     if (ev_fork) cudaEventDestroy(ev_fork);
     if (ev_join) cudaEventDestroy(ev_join);
     for (auto& e : ev_lat)
@@ -425,7 +436,7 @@ struct UnifiedFPNCore::Impl {
   // writes it (P5 / P2 lateral epilogue, P4 / P3 merge) and is quantised to e4m3 per image
   // on the side stream right before its 3x3 (per image, so an image's result does not
   // depend on the rest of its batch, e.g. on how a batch is sharded over GPUs):
-  //   main:  zero amax | lat5 (amax5) lat4 lat3 | merge4 (amax4) | merge3 (amax3) | lat2 + up(M3) (amax2)
+  //   main:  zero amax | lat5 (amax5) lat4 lat3 | merge4 (amax4) | merge3 (amax3, M3s) | lat2 + up(M3s) (amax2)
   //   side:              q5 3x3_5 (+P6)        q4 3x3_4         q3 3x3_3          q2 3x3_2
   int enqueue_e4m3(const void* const* in, void* const* out, void* p6, cudaStream_t main,
                    bool prof_events) {
@@ -441,19 +452,21 @@ struct UnifiedFPNCore::Impl {
     if (!prof_events) {
       check(cudaEventRecord(ev_fork, main), "event");
       check(cudaStreamWaitEvent(side, ev_fork, 0), "event");
+      for (int i = 0; i < 2; ++i) check(cudaStreamWaitEvent(lat_side[i], ev_fork, 0), "event");
     }
-    auto lateral = [&](int l, const void* coarse, unsigned* amax_out) {
+    auto lateral = [&](int l, const void* coarse, unsigned* amax_out, cudaStream_t st) {
       ufpn::TcScales sc;
       sc.ascale = in_scale[l];
       sc.wscale = lat_ws[l];
       sc.amax_out = amax_out;
+      sc.coarse_prescaled = coarse != nullptr;  // coarse = m3_scaled
       TcPlan p;
       check(ufpn::plan_tc_lateral(p, DType::E4M3, in[l], lat_wp[l], lat_b[l], coarse, merged[l],
                                   batch, cin[l], H[l], W[l], coarse ? H[l + 1] : 0,
                                   coarse ? W[l + 1] : 0, ufpn::default_tiling(H[l], W[l]),
                                   d_status, 0, sc),
             "plan e4m3 lateral");
-      ok(ufpn::launch_tc(p, main), "e4m3 lateral launch");
+      ok(ufpn::launch_tc(p, st), "e4m3 lateral launch");
     };
     auto conv_level = [&](int l) {
       if (!prof_events) {
@@ -475,22 +488,34 @@ struct UnifiedFPNCore::Impl {
             "plan e4m3 conv3x3");
       ok(ufpn::launch_tc(conv, conv_stream), "e4m3 conv3x3 launch");
     };
-    lateral(3, nullptr, fp8_amax + 3 * batch);
-    lateral(2, nullptr, nullptr);
-    lateral(1, nullptr, nullptr);
+    // The three raw laterals are independent GEMMs: P5 on the main stream, P4 and P3 on
+    // their own streams so the small P5 grid shares the machine with the larger ones.
+    lateral(3, nullptr, fp8_amax + 3 * batch, main);
+    for (int i = 0; i < 2; ++i) {
+      const cudaStream_t st = prof_events ? main : lat_side[i];
+      lateral(2 - i, nullptr, nullptr, st);
+      if (!prof_events) check(cudaEventRecord(ev_lat_done[i], st), "event");
+    }
     if (prof_events) cudaEventRecord(prof[1], main);
     conv_level(3);
     if (prof_events) cudaEventRecord(prof[2], main);
     for (int l = 2; l >= 1; --l) {
+      if (!prof_events) check(cudaStreamWaitEvent(main, ev_lat_done[2 - l], 0), "event");
+      // M3 also gets its copy pre-divided by the P2 lateral's per-channel scale, which the P2
+      // lateral adds through its tensor-core top-down k-block.
+      ufpn::MergeScaledCopy m3s;
+      m3s.out = m3_scaled;
+      m3s.scale_a = in_scale[0];
+      m3s.scale_w = lat_ws[0];
       ok(ufpn::launch_upsample_add(DType::BF16, merged[l + 1], merged[l], merged[l], batch, cout,
                                    H[l + 1], W[l + 1], H[l], W[l], 0, Layout::NHWC, main,
-                                   fp8_amax + l * batch),
+                                   fp8_amax + l * batch, l == 1 ? &m3s : nullptr),
          "merge");
       if (prof_events) cudaEventRecord(prof[3 + 2 * (2 - l)], main);
       conv_level(l);
       if (prof_events) cudaEventRecord(prof[4 + 2 * (2 - l)], main);
     }
-    lateral(0, merged[1], fp8_amax);
+    lateral(0, m3_scaled, fp8_amax, main);
     if (prof_events) cudaEventRecord(prof[7], main);
     conv_level(0);
     if (prof_events) cudaEventRecord(prof[8], main);
@@ -530,6 +555,10 @@ UnifiedFPNCore::UnifiedFPNCore(size_t workspace_size, int device) : impl_(new Im
   CUDA_CHECK(cudaStreamCreateWithFlags(&impl_->side, cudaStreamNonBlocking));
   CUDA_CHECK(cudaStreamCreateWithFlags(&impl_->capture, cudaStreamNonBlocking));
   CUDA_CHECK(cudaStreamCreateWithFlags(&impl_->setup, cudaStreamNonBlocking));
+  for (int i = 0; i < 2; ++i) {
+    CUDA_CHECK(cudaStreamCreateWithFlags(&impl_->lat_side[i], cudaStreamNonBlocking));
+    CUDA_CHECK(cudaEventCreateWithFlags(&impl_->ev_lat_done[i], cudaEventDisableTiming));
+  }
   CUDA_CHECK(cudaEventCreateWithFlags(&impl_->ev_fork, cudaEventDisableTiming));
   CUDA_CHECK(cudaEventCreateWithFlags(&impl_->ev_join, cudaEventDisableTiming));
   for (auto& e : impl_->ev_lat) CUDA_CHECK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
@@ -610,6 +639,9 @@ void UnifiedFPNCore::configure_levels(const std::vector<FPNDimensions>& dims, in
     m.check(cudaMalloc(&m.fp8_amax, 2 * words * sizeof(float)), "workspace");
     m.fp8_scale = reinterpret_cast<float*>(m.fp8_amax + words);
     total += 2 * words * sizeof(float);
+    const size_t px3 = static_cast<size_t>(N) * m.H[1] * m.W[1];
+    m.check(cudaMalloc(&m.m3_scaled, px3 * m.cout * 2), "workspace");
+    total += px3 * m.cout * 2;
   }
   if (m.tensor_core_path() && lay == Layout::NCHW) {
     const size_t px6 = static_cast<size_t>(N) * ((m.H[3] - 1) / 2 + 1) * ((m.W[3] - 1) / 2 + 1);

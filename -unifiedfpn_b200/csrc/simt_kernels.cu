@@ -92,6 +92,20 @@ __device__ __forceinline__ void publish_amax(unsigned* amax, unsigned bits) {
   if ((threadIdx.x & 31) == 0 && bits > *reinterpret_cast<volatile unsigned*>(amax))
     atomicMax(amax, bits);
 }
+// Block-wide version (every thread of the block must call it; red: blockDim/32 words of
+// shared memory): one guarded atomic per block.
+__device__ __forceinline__ void publish_amax_block(unsigned* amax, unsigned bits,
+                                                   unsigned* red) {
+  bits = __reduce_max_sync(0xffffffffu, bits);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = bits;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned m = 0;
+    for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) m = max(m, red[i]);
+    if (m > *reinterpret_cast<volatile unsigned*>(amax)) atomicMax(amax, m);
+  }
+  __syncthreads();
+}
 
 // ---------------------------------------------------------------- NHWC upsample-add
 // out[n,y,x,c] = lat[n,y,x,c] (or 0) + bilinear(coarse)[n,y,x,c].
@@ -186,20 +200,38 @@ __global__ void __launch_bounds__(256) upsample_add_nhwc_kernel(
 // one row, no loops; all five loads of a lane are independent and issued back to back.
 // `out` may alias `lat` (each lane reads its lateral vector before writing it).
 // amax (optional): amax[n] = atomicMax of |out| of image n as fp32 bits (for a following
-// per-image e4m3 quantisation).
+// per-image e4m3 quantisation).  out_s (optional): a second copy of out with channel c
+// multiplied by 1 / (scale_a[0] * scale_w[c]) (the e4m3 P2 lateral adds this copy through
+// its tensor-core top-down k-block before it scales its accumulator by the same factor).
 template <typename T>
 __global__ void __launch_bounds__(256) upsample_add_px512_kernel(
     const T* __restrict__ coarse, const T* lat, T* out, int N, int Hc, int Wc, int H, int W,
-    int chunks, float sy_scale, float sx_scale, int ac, unsigned* amax) {
+    int chunks, float sy_scale, float sx_scale, int ac, unsigned* amax, T* out_s,
+    const float* scale_a, const float* scale_w, int units_per_block) {
   static_assert(sizeof(T) == 2, "16-bit types");
+  __shared__ unsigned red[8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float inv[8];
+  if (out_s) {
+    const float sa = __ldg(scale_a);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) inv[e] = __frcp_rn(sa * __ldg(scale_w + lane * 8 + e));
+  }
   unsigned m = 0;
   int m_img = -1;  // image the running maximum m belongs to (block-uniform)
-  for (long long u = blockIdx.x; u < static_cast<long long>(N) * H * chunks; u += gridDim.x) {
+  // units_per_block == 0: one unit per block, strided (most loads in flight);
+  // > 0: a contiguous run of units per block, so a block crosses few image boundaries
+  // (one absmax publication per image it touches).
+  const long long total = static_cast<long long>(N) * H * chunks;
+  const long long u0 = units_per_block ? blockIdx.x * static_cast<long long>(units_per_block)
+                                       : blockIdx.x;
+  const long long u1 = units_per_block ? min(total, u0 + units_per_block) : total;
+  const long long du = units_per_block ? 1 : gridDim.x;
+  for (long long u = u0; u < u1; u += du) {
     const int r = static_cast<int>(u / chunks);
     const int n = r / H;
     if (amax && n != m_img) {
-      if (m_img >= 0) publish_amax(amax + m_img, m);
+      if (m_img >= 0) publish_amax_block(amax + m_img, m, red);
       m = 0;
       m_img = n;
     }
@@ -233,8 +265,14 @@ __global__ void __launch_bounds__(256) upsample_add_px512_kernel(
       m = max(m, abs_bits(to_f(o.e[e])));
     }
     *reinterpret_cast<uint4*>(out + io) = o.u;
+    if (out_s) {
+      Vec16<T> os;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) os.e[e] = from_f<T>(to_f(o.e[e]) * inv[e]);
+      *reinterpret_cast<uint4*>(out_s + io) = os.u;
+    }
   }
-  if (amax && m_img >= 0) publish_amax(amax + m_img, m);
+  if (amax && m_img >= 0) publish_amax_block(amax + m_img, m, red);
 }
 
 // ---------------------------------------------------------------- NCHW upsample-add
@@ -598,7 +636,7 @@ cudaError_t absmax_t(const void* x, long long n, int groups, unsigned* amax, cud
 template <typename T>
 cudaError_t upsample_add_t(const void* coarse, const void* lat, void* out, int N, int C, int Hc,
                            int Wc, int H, int W, int ac, Layout layout, cudaStream_t s,
-                           unsigned* amax) {
+                           unsigned* amax, const MergeScaledCopy* sc) {
   const float sy = (ac && H > 1) ? static_cast<float>(Hc - 1) / (H - 1)
                                  : static_cast<float>(Hc) / H;
   const float sx = (ac && W > 1) ? static_cast<float>(Wc - 1) / (W - 1)
@@ -614,12 +652,21 @@ cudaError_t upsample_add_t(const void* coarse, const void* lat, void* out, int N
       if (vec && C == 256) {
         const int chunks = (W + 7) / 8;
         const long long blocks = static_cast<long long>(N) * H * chunks;
-        const int grid = blocks < (1LL << 30) ? static_cast<int>(blocks) : (1 << 30);
+        int grid = blocks < (1LL << 30) ? static_cast<int>(blocks) : (1 << 30);
+        int per = 0;
+        if (amax) {  // contiguous runs: 8 resident 256-thread blocks per SM
+          const long long g = blocks < 148LL * 8 ? blocks : 148LL * 8;
+          per = static_cast<int>((blocks + g - 1) / g);
+          grid = static_cast<int>((blocks + per - 1) / per);
+        }
         upsample_add_px512_kernel<T>
-            <<<grid, 256, 0, s>>>(c, l, o, N, Hc, Wc, H, W, chunks, sy, sx, ac, amax);
+            <<<grid, 256, 0, s>>>(c, l, o, N, Hc, Wc, H, W, chunks, sy, sx, ac, amax,
+                                  sc ? static_cast<T*>(sc->out) : nullptr,
+                                  sc ? sc->scale_a : nullptr, sc ? sc->scale_w : nullptr, per);
         return cudaGetLastError();
       }
     }
+    if (sc) return cudaErrorNotSupported;  // the scaled copy exists on the 256-channel path
     const long long units =
         static_cast<long long>(N) * H * ((W + 8 * kUpPix - 1) / (8 * kUpPix));  // per block
     const int grid = units < 148 * 64 ? static_cast<int>(units) : 148 * 64;
@@ -631,6 +678,7 @@ cudaError_t upsample_add_t(const void* coarse, const void* lat, void* out, int N
           <<<grid, 256, 0, s>>>(c, l, o, N, C, Hc, Wc, H, W, sy, sx, ac);
   } else {
     const long long work = static_cast<long long>(N) * C * H * W;
+    if (sc) return cudaErrorNotSupported;
     upsample_add_nchw_kernel<T>
         <<<grid_for(work, 256), 256, 0, s>>>(c, l, o, N, C, Hc, Wc, H, W, sy, sx, ac);
   }
@@ -679,17 +727,21 @@ cudaError_t transpose_t(const void* in, void* out, int N, int C, int HW, bool to
 
 cudaError_t launch_upsample_add(DType dt, const void* coarse, const void* lat, void* out, int N,
                                 int C, int Hc, int Wc, int H, int W, int align_corners,
-                                Layout layout, cudaStream_t s, unsigned* amax_out) {
+                                Layout layout, cudaStream_t s, unsigned* amax_out,
+                                const MergeScaledCopy* scaled) {
+  if (scaled && (!scaled->out || !scaled->scale_a || !scaled->scale_w || !aligned16(scaled->out)))
+    return cudaErrorInvalidValue;
   switch (dt) {
     case DType::F32:
+      if (scaled) return cudaErrorNotSupported;
       return upsample_add_t<float>(coarse, lat, out, N, C, Hc, Wc, H, W, align_corners, layout, s,
-                                   amax_out);
+                                   amax_out, nullptr);
     case DType::F16:
       return upsample_add_t<__half>(coarse, lat, out, N, C, Hc, Wc, H, W, align_corners, layout,
-                                    s, amax_out);
+                                    s, amax_out, scaled);
     case DType::BF16:
       return upsample_add_t<__nv_bfloat16>(coarse, lat, out, N, C, Hc, Wc, H, W, align_corners,
-                                           layout, s, amax_out);
+                                           layout, s, amax_out, scaled);
     default:
       return cudaErrorInvalidValue;
   }

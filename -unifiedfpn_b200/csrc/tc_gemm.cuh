@@ -466,10 +466,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   // Top-down add through the tensor core (coarse box fits one k-block).
-  // (16-bit inputs only: the e4m3 epilogue scales the accumulator, which must then
-  // not already hold the unscaled top-down term.)
-  const bool bil_mma =
-      (kMode == 0) && !TcElem<T>::kFp8 && args.coarse != nullptr && args.cbox_w > 0;
+  // (e4m3 inputs: the planner enables it only for a coarse map pre-divided by the
+  // epilogue's per-channel scale, so the scaled accumulator holds the right top-down term.)
+  const bool bil_mma = (kMode == 0) && args.coarse != nullptr && args.cbox_w > 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {

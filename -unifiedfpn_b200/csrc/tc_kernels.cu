@@ -243,10 +243,10 @@ cudaError_t plan_tc_lateral(TcPlan& plan, DType dt, const void* x, const void* w
     // the accumulator is scaled in the epilogue, so the taps are added there.)
     const int ch = coarse_span(H, tiling.tile_h, a.scale_y, Hc);
     const int cw = coarse_span(W, tiling.tile_w, a.scale_x, Wc);
-    if (!fp8 && ch * cw <= kTcCoarseMaxPix) {
+    if ((!fp8 || sc.coarse_prescaled) && ch * cw <= kTcCoarseMaxPix) {
       a.cbox_h = ch;
       a.cbox_w = cw;
-      if ((e = encode_nhwc(&plan.map_coarse, dt, coarse, N, Hc, Wc, kTcBlockN, cw, ch)) !=
+      if ((e = encode_nhwc(&plan.map_coarse, odt, coarse, N, Hc, Wc, kTcBlockN, cw, ch)) !=
           cudaSuccess)
         return e;
     }

@@ -191,6 +191,11 @@ class UnifiedFPN:
         ordered, so a captured graph sees the same address every call)."""
         if input_scales is None or len(input_scales) < 4:
             raise ValueError("float8_e4m3fn inputs need input_scales for C2..C5")
+        if (isinstance(input_scales, torch.Tensor) and input_scales.is_cuda
+                and input_scales.device == self.device and input_scales.dtype == torch.float32
+                and input_scales.numel() == 4 and input_scales.is_contiguous()):
+            base = input_scales.data_ptr()  # the caller's own device array, used in place
+            return _ptr_array([base + 4 * l for l in range(4)])
         if self._scale_buf is None:
             self._scale_buf = torch.empty(4, dtype=torch.float32, device=self.device)
         vals = torch.stack([torch.as_tensor(s, dtype=torch.float32).reshape(()).to(self.device)
@@ -229,7 +234,7 @@ class UnifiedFPN:
     __call__ = forward
 
     # ------------------------------------------------------------------ tooling
-    def benchmark(self, backbone_features, num_iterations: int = 100):
+    def benchmark(self, backbone_features, num_iterations: int = 100, input_scales=None):
         """(avg_ms, GB/s, compute utilisation) of the neck, timed with CUDA events
         on the current stream (reference: fpn_pytorch.cpp:139-169 timed with the
         host clock)."""
@@ -237,32 +242,34 @@ class UnifiedFPN:
         outs, p6 = self._alloc_outputs(feats, mf, True)
         out = outs + [p6]
         for _ in range(10):
-            self.forward(feats, return_p6=True, out=out)
+            self.forward(feats, return_p6=True, out=out, input_scales=input_scales)
         s = torch.cuda.current_stream(self.device)
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(s)
         for _ in range(num_iterations):
-            self.forward(feats, return_p6=True, out=out)
+            self.forward(feats, return_p6=True, out=out, input_scales=input_scales)
         e1.record(s)
         e1.synchronize()
         ms = e0.elapsed_time(e1) / num_iterations
         esz = feats[0].element_size()
+        osz = out[0].element_size()
         nbytes = 0.0
         flops = 0.0
         for t in feats:
             px = t.shape[0] * t.shape[2] * t.shape[3]
-            nbytes += px * (t.shape[1] + 256) * esz
+            nbytes += px * (t.shape[1] * esz + 256 * osz)
             flops += 2.0 * px * 256 * (t.shape[1] + 9 * 256)
-        peak = 2.25e15 if feats[0].dtype != torch.float32 else 8.0e13
+        # nominal dense peaks: e4m3 4.5, bf16/fp16 2.25 PFLOP/s; fp32 CUDA cores 80 TFLOP/s
+        peak = {torch.float32: 8.0e13, E4M3: 4.5e15}.get(feats[0].dtype, 2.25e15)
         return ms, nbytes / (ms * 1e-3) / 1e9, flops / (ms * 1e-3) / peak
 
-    def get_performance_breakdown(self, backbone_features=None):
+    def get_performance_breakdown(self, backbone_features=None, input_scales=None):
         """[kernel_times_ms(8), metrics(5)] as in fpn_pytorch.cpp:171-187.  With
         ``backbone_features`` given, first runs one profiled (serialised) forward."""
         if backbone_features is not None:
             check(lib.ufpn_core_set_profiling(self._h, 1), "set_profiling")
-            self.forward(backbone_features, return_p6=True)
+            self.forward(backbone_features, return_p6=True, input_scales=input_scales)
         kt = (ctypes.c_float * 8)()
         mt = (ctypes.c_float * 5)()
         check(lib.ufpn_core_get_performance_metrics(self._h, kt, mt), "get_performance_metrics")

@@ -32,6 +32,7 @@ sys.path.insert(0, str(ROOT / "-unifiedfpn_b200"))
 import torch  # noqa: E402
 
 METRIC = "FPN-neck images/sec, R50 800×1216 bf16 @1/2/4/8 B200; % of roofline"
+METRIC_FP8 = "FPN-neck images/sec, FP8 (e4m3) R50 640×640, 16 images/GPU @1/2/4/8 B200; % of roofline"
 R50_CHANNELS = (256, 512, 1024, 2048)
 
 
@@ -47,14 +48,15 @@ def neck_flops(batch, chans, sizes):
     return f
 
 
-def neck_bytes(batch, chans, sizes, esz):
-    """Compulsory HBM bytes: read C2..C5 and weights, write P2..P6."""
+def neck_bytes(batch, chans, sizes, esz, out_esz=None):
+    """Compulsory HBM bytes: read C2..C5 and weights (esz), write P2..P6 (out_esz)."""
+    out_esz = esz if out_esz is None else out_esz
     b = 0.0
     for c, (h, w) in zip(chans, sizes):
         px = batch * h * w
-        b += px * (c + 256) * esz + (256 * c + 9 * 256 * 256) * esz
+        b += px * c * esz + px * 256 * out_esz + (256 * c + 9 * 256 * 256) * esz
     h5, w5 = sizes[3]
-    b += batch * ((h5 + 1) // 2) * ((w5 + 1) // 2) * 256 * esz
+    b += batch * ((h5 + 1) // 2) * ((w5 + 1) // 2) * 256 * out_esz
     return b
 
 
@@ -148,7 +150,8 @@ class ClockSampler:
 
 
 def cpu_baseline(seconds=12.0, image=(800, 1216)):
-    """The CPU oracle neck (fp32, torch CPU, all host threads) on one image per iteration."""
+    """The CPU oracle neck (fp32, torch CPU, all host threads) on one image per iteration
+    of the workload's image size."""
     from oracle import fpn_oracle as O
     torch.set_num_threads(os.cpu_count() or 1)
     sizes = level_sizes(*image)
@@ -164,7 +167,7 @@ def cpu_baseline(seconds=12.0, image=(800, 1216)):
             if el >= seconds or n >= 50:
                 break
     return {"value": n / el, "unit": "images/s", "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{n} x 1 image R50 800x1216 fp32 (torch CPU oracle neck, {el:.1f} s)"}
+            "sample": f"{n} x 1 image R50 {image[0]}x{image[1]} fp32 (torch CPU oracle neck, {el:.1f} s)"}
 
 
 def run_reference(args, rank, world):
@@ -207,16 +210,26 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--batch", type=int, default=2, help="images per GPU")
-    ap.add_argument("--height", type=int, default=800)
-    ap.add_argument("--width", type=int, default=1216)
-    ap.add_argument("--dtype", choices=["bf16", "fp16"], default="bf16")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="images per GPU (default 2; 16 for e4m3)")
+    ap.add_argument("--height", type=int, default=None, help="default 800 (640 for e4m3)")
+    ap.add_argument("--width", type=int, default=None, help="default 1216 (640 for e4m3)")
+    ap.add_argument("--dtype", choices=["bf16", "fp16", "e4m3"], default="bf16",
+                    help="e4m3: the FP8 neck on e4m3 inputs (bf16 outputs), R50 640x640, "
+                         "16 images/GPU by default")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-roofline", action="store_true")
     ap.add_argument("--schedule", choices=["fused", "split"], default="split",
                     help="one persistent neck kernel, or eight per-level kernels on two streams")
     args = ap.parse_args()
+    fp8 = args.dtype == "e4m3"
+    if args.batch is None:
+        args.batch = 16 if fp8 else 2
+    if args.height is None:
+        args.height = 640 if fp8 else 800
+    if args.width is None:
+        args.width = 640 if fp8 else 1216
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
 
@@ -235,28 +248,39 @@ def main():
 
     import unified_fpn as U
 
-    dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float16
-    esz = 2
+    fp8 = args.dtype == "e4m3"
+    dtype = {"bf16": torch.bfloat16, "fp16": torch.float16, "e4m3": torch.float8_e4m3fn}[args.dtype]
+    esz = 1 if fp8 else 2
+    out_esz = 2
     sizes = level_sizes(args.height, args.width)
     B = args.batch
-    n_sets = 3  # rotating input sets: 3 x ~117 MB of C2..C5 > 126 MB L2
+    n_sets = 3  # rotating input sets, together larger than the 126 MB L2
     gen = torch.Generator(device=dev)
-    feats = []
+    feats, scales = [], []
     for s in range(n_sets):
         gen.manual_seed(1000 * rank + s)
-        feats.append([torch.randn(B, c, h, w, device=dev, generator=gen, dtype=torch.float32).clamp_min_(0)
-                      .to(dtype).contiguous(memory_format=torch.channels_last)
-                      for c, (h, w) in zip(R50_CHANNELS, sizes)])
+        if fp8:
+            # seeded N(0,1) features, quantised per tensor (scale = absmax / 448) on the device
+            qs = [U.quantize_fp8(torch.randn(B, c, h, w, device=dev, generator=gen).contiguous(
+                memory_format=torch.channels_last)) for c, (h, w) in zip(R50_CHANNELS, sizes)]
+            feats.append([q for q, _ in qs])
+            scales.append(torch.cat([sc for _, sc in qs]))
+        else:
+            feats.append([torch.randn(B, c, h, w, device=dev, generator=gen, dtype=torch.float32)
+                          .clamp_min_(0).to(dtype).contiguous(memory_format=torch.channels_last)
+                          for c, (h, w) in zip(R50_CHANNELS, sizes)])
+            scales.append(None)
+    in_mb = sum(B * c * h * w * esz for c, (h, w) in zip(R50_CHANNELS, sizes)) / 1e6
     fpn = U.UnifiedFPN(device=dev)
     fpn.set_schedule(fused_neck_kernel=args.schedule == "fused")
     outs = []
     for s in range(n_sets):
-        o = fpn(feats[s], return_p6=True)
+        o = fpn(feats[s], return_p6=True, input_scales=scales[s])
         outs.append(o)
     torch.cuda.synchronize(dev)
 
     def step(i):
-        fpn(feats[i % n_sets], return_p6=True, out=outs[i % n_sets])
+        fpn(feats[i % n_sets], return_p6=True, out=outs[i % n_sets], input_scales=scales[i % n_sets])
 
     for i in range(args.warmup):
         step(i)
@@ -288,77 +312,93 @@ def main():
     ms_per_step = ms / args.steps
 
     # ---------------------------------------------------------------- e2e through the public API
+    # Host-resident batches streamed through unified_fpn.HostPipeline: every step copies its
+    # C2..C5 (and e4m3 scales) from pinned host memory and P2..P6 back to pinned host memory;
+    # step i's neck overlaps step i+1's copy-in and step i-1's copy-out.
     e2e = None
     if not args.no_e2e:
+        pipe = U.HostPipeline(fpn, feats[0], return_p6=True, depth=2)
         host_in = [f.cpu().pin_memory() for f in feats[0]]
-        host_out = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs[0]]
-        dev_in = [torch.empty_like(f) for f in feats[0]]
-        h2d = sum(t.numel() * t.element_size() for t in host_in)
-        d2h = sum(t.numel() * t.element_size() for t in host_out)
-
-        def e2e_step():
-            for d, h in zip(dev_in, host_in):
-                d.copy_(h, non_blocking=True)  # NHWC strides are preserved
-            res = fpn(dev_in, return_p6=True, out=outs[0])
-            for h, r in zip(host_out, res):
-                h.copy_(r, non_blocking=True)
-
-        for _ in range(2):
-            e2e_step()
-        n_e2e = max(3, min(args.steps, 10))
+        host_sc = scales[0].cpu().pin_memory() if fp8 else None
+        host_out = [pipe.host_buffers() for _ in range(2)]
+        h2d = sum(t.numel() * t.element_size() for t in host_in) + (16 if fp8 else 0)
+        d2h = sum(t.numel() * t.element_size() for t in host_out[0])
+        for k in range(4):
+            pipe.submit(host_in, host_out[k % 2], host_sc)
+        pipe.synchronize()
+        n_e2e = max(6, min(args.steps, 20))
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
         a0 = torch.cuda.Event(enable_timing=True)
         a1 = torch.cuda.Event(enable_timing=True)
         a0.record(stream)
-        for _ in range(n_e2e):
-            e2e_step()
+        pipe.fork(stream)
+        for k in range(n_e2e):
+            pipe.submit(host_in, host_out[k % 2], host_sc)
+        pipe.join(stream)
         a1.record(stream)
         torch.cuda.synchronize(dev)
         ems, e_images = job_throughput(a0.elapsed_time(a1), B * n_e2e, world, dev)
         e2e = {"value": e_images / (ems / 1e3), "unit": "images/s", "h2d_bytes_per_step": h2d,
-               "d2h_bytes_per_step": d2h, "steps": n_e2e}
+               "d2h_bytes_per_step": d2h, "steps": n_e2e,
+               "api": "unified_fpn.HostPipeline (copy-in / neck / copy-out overlapped across steps)"}
 
     # ---------------------------------------------------------------- roofline of the dominant kernel
     roofline = None
     peaks = measured_peaks()
     kernel_share = None
     if not args.no_roofline:
-        kt, mt = fpn.get_performance_breakdown(feats[0])  # one serialised, event-timed forward
+        kt, mt = fpn.get_performance_breakdown(feats[0], input_scales=scales[0])  # serialised, event-timed
         total = float(kt.sum().item())
         from unified_fpn.helpers import STAGES_TC
         kernel_share = {n: {"ms": round(float(v), 4), "share": round(float(v) / total, 4)}
                         for n, v in zip(STAGES_TC, kt.tolist())} if total > 0 else None
         h2, w2 = sizes[0]
-        x = torch.randn(B, 256, h2, w2, device=dev, generator=gen).to(dtype).contiguous(
+        xr = torch.randn(B, 256, h2, w2, device=dev, generator=gen).contiguous(
             memory_format=torch.channels_last)
-        wt = U.pack_conv3x3_weight(torch.randn(256, 256, 3, 3, device=dev, generator=gen) * 0.03, dtype)
+        w3 = torch.randn(256, 256, 3, 3, device=dev, generator=gen) * 0.03
         bias = torch.zeros(256, device=dev)
+        if fp8:
+            xq, xs = U.quantize_fp8(xr, per_image=True)
+            wq, wsc = U.quantize_fp8_rows(w3, pack3x3=True)
+            conv = lambda: U.fpn_conv3x3_fp8(xq, xs, wq, wsc, bias)  # noqa: E731
+        else:
+            x = xr.to(dtype)
+            wt = U.pack_conv3x3_weight(w3, dtype)
+            conv = lambda: U.fpn_conv3x3(x, wt, bias)  # noqa: E731
         reps = 20
         for _ in range(3):
-            U.fpn_conv3x3(x, wt, bias)
+            conv()
         r0 = torch.cuda.Event(enable_timing=True)
         r1 = torch.cuda.Event(enable_timing=True)
         r0.record(stream)
         for _ in range(reps):
-            U.fpn_conv3x3(x, wt, bias)
+            conv()
         r1.record(stream)
         torch.cuda.synchronize(dev)
         kms = r0.elapsed_time(r1) / reps
         flops = 2.0 * B * h2 * w2 * 256 * 256 * 9
         achieved = flops / (kms * 1e-3) / 1e12
-        traffic = profile_traffic("conv3x3_p2_r50_800x1216_b2")
-        roofline = {"kernel": f"conv3x3 P2 implicit GEMM (tcgen05), {B}x{h2}x{w2}x256 -> 256",
-                    "bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"],
-                    "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
-                    "peak_src": f"{peaks['src']} bf16 burst (kernel timed alone)",
+        # e4m3 runs at twice the bf16 dense rate; no e4m3 GEMM peak is measured on this
+        # pool, so its peak is derived as 2 x the measured bf16 figures.
+        mult = 2.0 if fp8 else 1.0
+        peak = peaks["bf16_tflops"] * mult
+        traffic = profile_traffic("conv3x3_fp8_p2_r50_640x640_b16" if fp8
+                                  else "conv3x3_p2_r50_800x1216_b2")
+        roofline = {"kernel": f"conv3x3 P2 implicit GEMM (tcgen05 {'kind::f8f6f4' if fp8 else 'kind::f16'}),"
+                              f" {B}x{h2}x{w2}x256 -> 256",
+                    "bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
+                    "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                    "peak_src": (f"derived: 2 x {peaks['src']} bf16 burst" if fp8
+                                 else f"{peaks['src']} bf16 burst (kernel timed alone)"),
                     "launch_ms": round(kms, 4), "flops_per_launch": flops, "traffic": traffic,
                     "neck_frac_of_roofline": None}
         # whole-neck roofline: slower of FLOPs at the sustained tensor peak and bytes at HBM peak
         f_all = neck_flops(B, R50_CHANNELS, sizes)
-        b_all = neck_bytes(B, R50_CHANNELS, sizes, esz)
-        t_roof = max(f_all / (peaks["bf16_tflops_sustained"] * 1e12), b_all / (peaks["hbm_gbs"] * 1e9))
+        b_all = neck_bytes(B, R50_CHANNELS, sizes, esz, out_esz)
+        t_roof = max(f_all / (peaks["bf16_tflops_sustained"] * mult * 1e12),
+                     b_all / (peaks["hbm_gbs"] * 1e9))
         roofline["neck_frac_of_roofline"] = round(t_roof * 1e3 / ms_per_step, 4)
         roofline["neck_roofline_ms"] = round(t_roof * 1e3, 4)
 
@@ -369,18 +409,22 @@ def main():
 
     cpu = None
     if rank == 0 and not args.no_cpu_baseline and world == 1:
-        cpu = cpu_baseline()
+        cpu = cpu_baseline(image=(args.height, args.width))
 
     if rank == 0:
+        data = ("synthetic (seeded N(0,1) features quantised per tensor to e4m3 on the device; "
+                "random Kaiming-normal weights quantised per output channel)" if fp8 else
+                "synthetic (seeded N(0,1) after ReLU clamp; random Kaiming-normal weights)")
         line = {
-            "metric": METRIC, "value": round(value, 2), "unit": "images/s", "n_gpus": world, "steps": args.steps,
+            "metric": METRIC_FP8 if fp8 else METRIC, "value": round(value, 2), "unit": "images/s",
+            "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": args.dtype,
-            "data": "synthetic (seeded N(0,1) after ReLU clamp; random Kaiming-normal weights)",
-            "config": {"workload": f"R50 FPN neck {args.height}x{args.width}, {B} images/GPU, {args.dtype} NHWC",
+            "scaling": "weak", "vs_baseline": None, "dtype": args.dtype, "data": data,
+            "config": {"workload": f"R50 FPN neck {args.height}x{args.width}, {B} images/GPU, {args.dtype} NHWC"
+                                   + (" (bf16 outputs)" if fp8 else ""),
                        "global_batch": B * world, "per_gpu_batch": B,
                        "levels": [[B, c, h, w] for c, (h, w) in zip(R50_CHANNELS, sizes)],
-                       "l2": f"inputs rotate over {n_sets} sets (~{n_sets * 117} MB at 800x1216 b2) > 126 MB L2",
+                       "l2": f"inputs rotate over {n_sets} sets ({n_sets} x {in_mb:.0f} MB) > 126 MB L2",
                        "parallelism": f"dp{world} batch shards, no collective on the data path"},
             "clocks": clk, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
             "schedule": args.schedule, "neck_timeline_us": timeline,

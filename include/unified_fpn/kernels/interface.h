@@ -32,11 +32,19 @@ inline int dtype_size(DType d) {
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // ---- bandwidth kernels (simt_kernels.cu)
+// A second, per-channel scaled copy of an upsample-add result: out[c] / (scale_a[0] *
+// scale_w[c]), same layout (NHWC, 256 channels of a 16-bit type only).
+struct MergeScaledCopy {
+  void* out = nullptr;
+  const float* scale_a = nullptr;  // device scalar
+  const float* scale_w = nullptr;  // device [256]
+};
 // amax_out (optional): amax_out[n] = atomicMax of |out| of image n as fp32 bits (the caller
-// zeroes them first).
+// zeroes them first).  scaled (optional): also write the scaled copy.
 cudaError_t launch_upsample_add(DType dt, const void* coarse, const void* lat, void* out, int N,
                                 int C, int Hc, int Wc, int H, int W, int align_corners,
-                                Layout layout, cudaStream_t s, unsigned* amax_out = nullptr);
+                                Layout layout, cudaStream_t s, unsigned* amax_out = nullptr,
+                                const MergeScaledCopy* scaled = nullptr);
 // ---- e4m3 quantisation (simt_kernels.cu).  scale = amax / 448, q = e4m3_rn_satfinite(
 // x * (448 / amax)) (amax == 0: scale = 1, q = 0); amax carried as fp32 bits.
 // The n elements form `groups` equal consecutive groups (images), each with its own
@@ -109,6 +117,10 @@ struct TcScales {
   bool ascale_per_image = false;  // ascale[n] per image, else ascale[0] for the tensor
   const float* wscale = nullptr;  // per-output-channel weight scales [256], 16-byte aligned
   unsigned* amax_out = nullptr;   // [N] (device), zeroed by the caller
+  // E4M3 lateral with a coarse map: the coarse map is already divided by (ascale[0] *
+  // wscale[c]) per channel (MergeScaledCopy), so the top-down add can run as a tensor-core
+  // k-block on the unscaled accumulator.  Otherwise the epilogue adds it from global memory.
+  bool coarse_prescaled = false;
 };
 
 // Lateral 1x1 (+ optional fused bilinear upsample-add of the coarser merged map).

@@ -274,10 +274,16 @@ def fpn_neck_e4m3(q_feats, in_scales, qw: NeckWeightsE4M3, return_merged: bool =
     for l in (3, 2, 1, 0):
         x = q_feats[l].double()
         acc = F.conv2d(x, qw.lat_q[l].double().reshape(256, -1, 1, 1))
-        cs = (torch.tensor(np.float32(in_scales[l])).float() * qw.lat_s[l]).double()  # fp32 product
+        cs32 = torch.tensor(np.float32(in_scales[l])).float() * qw.lat_s[l]  # fp32 product
+        cs = cs32.double()
         m = acc * cs.reshape(1, -1, 1, 1) + qw.lat_b[l].double().reshape(1, -1, 1, 1)
         if l == 0:
-            m = _bf16((m + bilinear_upsample_t(merged[1].double(), m.shape[-2:])).float())
+            # The P2 top-down term enters the unscaled accumulator as bilinear(M3s) with
+            # M3s = bf16(M3 * fp32(1 / cs)) per channel; the epilogue's scale restores it.
+            inv = (torch.ones(256) / cs32).reshape(1, -1, 1, 1)
+            m3s = _bf16(merged[1] * inv)
+            up = bilinear_upsample_t(m3s.double(), m.shape[-2:]) * cs.reshape(1, -1, 1, 1)
+            m = _bf16((m + up).float())
         elif l < 3:
             m = _bf16((_bf16(m.float()).double() + bilinear_upsample_t(merged[l + 1].double(),
                                                                         m.shape[-2:])).float())

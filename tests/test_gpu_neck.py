@@ -180,3 +180,33 @@ def test_errors_are_raised_not_exit(cuda_device):
         fpn.set_kernel_config(tile_size=24)
     with pytest.raises(ValueError):
         U.UnifiedFPN(output_channels=128)
+
+
+@pytest.mark.parametrize("fp8", [False, True])
+def test_host_pipeline_matches_forward(cuda_device, fp8):
+    """HostPipeline (copy-in / neck / copy-out overlapped across batches) returns, for
+    every batch, exactly what a plain forward of that batch returns."""
+    import unified_fpn as U
+    chans, sizes = O.R50_CHANNELS, O.level_sizes(128, 160)
+    fpn = U.UnifiedFPN()
+    batches, scales = [], []
+    for k in range(5):
+        fs = [_cl(f.cuda()) for f in O.make_features(2, chans, sizes, seed=50 + k, dist="normal")]
+        if fp8:
+            qs = [U.quantize_fp8(f) for f in fs]
+            batches.append([q for q, _ in qs])
+            scales.append(torch.cat([s for _, s in qs]))
+        else:
+            batches.append([f.to(torch.bfloat16) for f in fs])
+            scales.append(None)
+    expect = [[o.cpu() for o in fpn(b, return_p6=True, input_scales=s)] for b, s in zip(batches, scales)]
+    pipe = U.HostPipeline(fpn, batches[0], return_p6=True, depth=2)
+    outs = [pipe.host_buffers() for _ in batches]
+    for b, s, o in zip(batches, scales, outs):
+        pipe.submit([t.cpu().pin_memory() for t in b], o,
+                    s.cpu().pin_memory() if s is not None else None)
+    pipe.synchronize()
+    assert fpn.device_status() == 0
+    for e, o in zip(expect, outs):
+        for a, b in zip(e, o):
+            assert torch.equal(a, b)
