@@ -338,8 +338,11 @@ int ufpn_conv3x3(int dtype, const void* x, const void* w, const float* bias, voi
     t.tile_w = tile_w;
     t.tile_h = 128 / tile_w;
     t.halo = false;
+  } else if (tile_w == -1) {
+    t = ufpn::halo_pair_tiling();
   } else if (tile_w < 0) {
-    return fail(UFPN_ERR_INVALID_ARG, "tile_w must be 0 (halo tiling) or 8..128");
+    return fail(UFPN_ERR_INVALID_ARG,
+                "tile_w must be 0 (halo tiling), -1 (halo tiling on CTA pairs) or 8..128");
   }
   int* status = device_status_word();
   ufpn::TcPlan plan;
@@ -479,7 +482,7 @@ int ufpn_lateral_conv_e4m3(const void* x, const float* x_scale, int x_scale_per_
 
 int ufpn_conv3x3_e4m3(const void* x, const float* x_scale, int x_scale_per_image, const void* w,
                       const float* w_scales, const float* bias, void* out, void* p6, int N,
-                      int H, int W, unsigned* amax_out, void* stream) {
+                      int H, int W, int tile_w, unsigned* amax_out, void* stream) {
   if (!x || !x_scale || !w || !w_scales || !bias || !out)
     return fail(UFPN_ERR_INVALID_ARG, "NULL tensor pointer");
   if (N <= 0 || H <= 0 || W <= 0) return fail(UFPN_ERR_INVALID_ARG, "sizes must be positive");
@@ -491,9 +494,13 @@ int ufpn_conv3x3_e4m3(const void* x, const float* x_scale, int x_scale_per_image
   sc.ascale_per_image = x_scale_per_image != 0;
   sc.wscale = w_scales;
   sc.amax_out = amax_out;
+  if (tile_w != 0 && tile_w != -1)
+    return fail(UFPN_ERR_INVALID_ARG, "e4m3 3x3: tile_w must be 0 (halo) or -1 (halo, CTA pairs)");
   ufpn::TcPlan plan;
   cudaError_t e = ufpn::plan_tc_conv3x3(plan, DType::E4M3, x, w, bias, out, p6, N, H, W,
-                                        ufpn::halo_tiling(), device_status_word(), 0, sc);
+                                        tile_w == -1 ? ufpn::halo_pair_tiling()
+                                                     : ufpn::halo_tiling(),
+                                        device_status_word(), 0, sc);
   if (e != cudaSuccess) return cuda_fail(e, "plan e4m3 conv3x3");
   e = ufpn::launch_tc(plan, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "e4m3 conv3x3 launch");

@@ -1,0 +1,235 @@
+// 3x3 conv with halo reuse on CTA PAIRS (tcgen05 cta_group::2).
+//
+// Same math, tiles and epilogue as fpn_conv3x3_halo_kernel (tc_gemm.cuh), but the two CTAs
+// of a (2,1,1) cluster run ONE tcgen05.mma stream of M = 256 rows: the leader's 8x16 tile
+// (rows 0..127) and the next tile (rows 128..255, the peer's).  Each CTA stages its own
+// tile's halo (A) and HALF of every weight k-block (B: output channels 128*rank..+127), so
+// the weight stream each SM pulls from L2 per tile halves; the leader issues the MMAs,
+// which read both CTAs' shared memory and write each CTA's 128 accumulator lanes in its
+// own TMEM.
+//
+// Synchronisation (all waits bounded, as everywhere in this library):
+//   full[s], hfull[h]  leader's barriers; the leader's producer arms them with BOTH CTAs'
+//                      byte counts, both producers' TMA loads complete on them
+//   empty[s], hempty[h] per CTA; the leader's MMA thread releases a stage in both CTAs
+//                      with one tcgen05.commit to the same offset in both
+//   accf[a]            per CTA, same commit; the epilogue of each CTA waits on its own
+//   acce[a]            leader's; 16 warp arrivals (8 epilogue warps per CTA)
+// A cluster barrier after initialisation and another before TMEM is released keep either
+// CTA from touching the other's shared memory or TMEM outside their lifetimes.
+#pragma once
+
+#include "tc_gemm.cuh"
+
+namespace ufpn {
+
+constexpr int kPairBStage = (kTcBlockN / 2) * 128;  // half of a weight k-block: 16 KB
+constexpr int kPairStages = 8;
+struct PairCfg {
+  static constexpr int kOffHalo = kPairStages * kPairBStage;
+  static constexpr int kOffStaging = kOffHalo + kHaloBufs * kHaloBytes;
+  static constexpr int kOffBars = kOffStaging + kTcEpiWarps * kTcStagingPerWarp;
+  static constexpr int kSmemBytes = kOffBars + 512 + 1024;
+};
+static_assert(PairCfg::kSmemBytes <= 232448, "pair smem");
+
+template <typename T>
+__device__ __forceinline__ void tc_mma_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  if constexpr (TcElem<T>::kFp8)
+    tc_mma_f8_pair(d_tmem, adesc, bdesc, idesc, accumulate);
+  else
+    tc_mma_f16_pair(d_tmem, adesc, bdesc, idesc, accumulate);
+}
+
+// Bounded idle wait (teardown after an abort: lets copies already in flight land).
+__device__ __forceinline__ void pair_settle_ns(uint64_t ns) {
+  const uint64_t t0 = globaltimer_ns();
+  while (globaltimer_ns() - t0 < ns) {
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    fpn_conv3x3_halo_pair_kernel(const __grid_constant__ CUtensorMap map_a,
+                                 const __grid_constant__ CUtensorMap map_b,
+                                 const __grid_constant__ CUtensorMap map_out,
+                                 const TcGemmArgs args) {
+  constexpr int S = kPairStages;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  // Both CTAs compute the same aligned offset (same dynamic shared memory layout).
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint8_t* smem_b = smem;
+  uint8_t* smem_halo = smem + PairCfg::kOffHalo;
+  uint8_t* smem_stage = smem + PairCfg::kOffStaging;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + PairCfg::kOffBars);
+  uint64_t* full_bar = bars;
+  uint64_t* empty_bar = bars + S;
+  uint64_t* hfull_bar = bars + 2 * S;
+  uint64_t* hempty_bar = hfull_bar + kHaloBufs;
+  uint64_t* accf_bar = hempty_bar + kHaloBufs;
+  uint64_t* acce_bar = accf_bar + 2;
+  uint64_t* done_bar = acce_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cin_blocks = args.cin_blocks;
+  const int units = (args.num_tiles + 1) / 2;
+  const int u0 = static_cast<int>(blockIdx.x >> 1);
+  const int ustep = static_cast<int>(gridDim.x >> 1);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int h = 0; h < kHaloBufs; ++h) {
+      mbar_init(&hfull_bar[h], 1);
+      mbar_init(&hempty_bar[h], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf_bar[b], 1);
+      mbar_init(&acce_bar[b], 2 * kTcEpiWarps);
+    }
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&map_a);
+    prefetch_tmap(&map_b);
+    prefetch_tmap(&map_out);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, kTcTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers initialised and TMEM allocated in BOTH CTAs
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (each CTA)
+    if (lane == 0) {
+      int stage = 0, hb = 0;
+      uint32_t phase = 0, hphase = 0;
+      bool ok = true;
+      const uint32_t full0 = mapa_shared(smem_u32(full_bar), 0);
+      const uint32_t hfull0 = mapa_shared(smem_u32(hfull_bar), 0);
+      const int brow = static_cast<int>(rank) * (kTcBlockN / 2);
+      for (int u = u0; ok && u < units; u += ustep) {
+        int n, x0, y0;
+        tc_tile_origin(args, 2 * u + static_cast<int>(rank), n, x0, y0);
+        for (int cb = 0; ok && cb < cin_blocks; ++cb) {
+          if (!mbar_wait(&hempty_bar[hb], hphase ^ 1u, abort_flag, args.status,
+                         kDevTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(&hfull_bar[hb], 2 * kHaloRows * 128);
+          tma_load_4d_pair(smem_halo + hb * kHaloBytes, &map_a, hfull0 + hb * 8u,
+                           cb * kKbElems<T>, x0 - 1, y0 - 1, n, kPolicyEvictLast);
+          if (++hb == kHaloBufs) {
+            hb = 0;
+            hphase ^= 1u;
+          }
+          for (int tap = 0; tap < 9; ++tap) {
+            if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, args.status,
+                           kDevTimeoutProducer)) {
+              ok = false;
+              break;
+            }
+            if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * kPairBStage);
+            tma_load_2d_pair(smem_b + stage * kPairBStage, &map_b, full0 + stage * 8u,
+                             (tap * cin_blocks + cb) * kKbElems<T>, brow, kPolicyEvictLast);
+            if (++stage == S) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          }
+        }
+      }
+      // Copies in flight complete on the leader's barriers; after an abort, give them time
+      // to land before this CTA's shared memory can go away.
+      if (!ok) pair_settle_ns(1000000);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader)
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc =
+          make_idesc(2 * kTcBlockM, kTcBlockN, TcElem<T>::kFmt, TcElem<T>::kFmt);
+      int stage = 0, hb = 0, acc = 0;
+      uint32_t phase = 0, hphase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int u = u0; ok && u < units; u += ustep) {
+        if (!mbar_wait(&acce_bar[acc], acc_phase ^ 1u, abort_flag, args.status, kDevTimeoutMma))
+          break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kTcBlockN);
+        for (int cb = 0; ok && cb < cin_blocks; ++cb) {
+          if (!mbar_wait(&hfull_bar[hb], hphase, abort_flag, args.status, kDevTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t halo_addr = smem_u32(smem_halo + hb * kHaloBytes);
+          for (int tap = 0; tap < 9; ++tap) {
+            if (!mbar_wait(&full_bar[stage], phase, abort_flag, args.status, kDevTimeoutMma)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const int dy = tap / 3, dx = tap % 3;
+            const uint64_t adesc = sdesc_kmajor_sw128_stride(
+                halo_addr + static_cast<uint32_t>((dy * (kHaloTileW + 2) + dx) * 128),
+                (kHaloTileW + 2) * 128);
+            const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(smem_b + stage * kPairBStage));
+#pragma unroll
+            for (int k = 0; k < kMmaPerKb; ++k)
+              tc_mma_pair<T>(d_tmem, adesc + 2u * k, bdesc + 2u * k, idesc,
+                             (cb > 0 || tap > 0 || k > 0) ? 1u : 0u);
+            tc_commit_pair_both(&empty_bar[stage]);
+            if (++stage == S) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          }
+          if (!ok) break;
+          tc_commit_pair_both(&hempty_bar[hb]);
+          if (++hb == kHaloBufs) {
+            hb = 0;
+            hphase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair_both(&accf_bar[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      // Every MMA issued must finish before either CTA releases its TMEM.
+      tc_commit_pair_local(done_bar);
+      mbar_wait_drain(done_bar, 0);
+    }
+  } else {
+    tc_epilogue<1, T, true>(args, &map_out, tmem_base, accf_bar, acce_bar, smem_stage,
+                            abort_flag, warp, lane, false,
+                            mapa_shared(smem_u32(acce_bar), 0));
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the leader's MMAs are drained; no CTA touches the other any more
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTcTmemCols);
+  }
+}
+
+}  // namespace ufpn

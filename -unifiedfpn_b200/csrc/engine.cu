@@ -62,9 +62,13 @@ DType to_dtype(FPNDataType t) {
   }
 }
 
-// 3x3 tiling from its tuning code: 0 = halo reuse with 8 x 16 tiles (the default),
-// 8..128 = plain tiles of that width (one shifted box per tap).
+// 3x3 tiling from its tuning code: -1 = halo tiles on CTA pairs (the default), 0 = halo
+// reuse with 8 x 16 tiles on single CTAs, 8..128 = plain tiles of that width (one shifted
+// box per tap).
+constexpr int kDefaultTilingCode = -1;
+int tiling_code(const Conv3x3Tiling& t) { return t.pair ? -1 : (t.halo ? 0 : t.tile_w); }
 Conv3x3Tiling tiling_from_code(int tw) {
+  if (tw == -1) return ufpn::halo_pair_tiling();
   if (tw <= 0) return ufpn::halo_tiling();
   Conv3x3Tiling t;
   t.tile_w = tw;
@@ -482,8 +486,10 @@ struct UnifiedFPNCore::Impl {
       sc.ascale_per_image = true;
       sc.wscale = out_ws[l];
       TcPlan conv;
+      Conv3x3Tiling t = tiling_for(l);
+      if (!t.halo) t = ufpn::halo_pair_tiling();  // e4m3 runs halo tiles only
       check(ufpn::plan_tc_conv3x3(conv, DType::E4M3, qmerged[l], out_wp[l], out_b[l], out[l],
-                                  l == 3 ? p6 : nullptr, batch, H[l], W[l], ufpn::halo_tiling(),
+                                  l == 3 ? p6 : nullptr, batch, H[l], W[l], t,
                                   d_status, 0, sc),
             "plan e4m3 conv3x3");
       ok(ufpn::launch_tc(conv, conv_stream), "e4m3 conv3x3 launch");
@@ -609,7 +615,7 @@ void UnifiedFPNCore::configure_levels(const std::vector<FPNDimensions>& dims, in
     m.cin[l] = dims[l].channels;
     m.H[l] = dims[l].height;
     m.W[l] = dims[l].width;
-    m.tiling[l] = ufpn::halo_tiling();
+    m.tiling[l] = tiling_from_code(kDefaultTilingCode);
     m.tiling_tuned[l] = false;
     auto it = m.tuning_db.find(m.tuning_key(l));
     if (it != m.tuning_db.end()) {
@@ -888,7 +894,7 @@ std::string UnifiedFPNCore::autotune(const void* const* in, void* const* out, vo
     return rep.str();
   }
   if (m.dtype == DType::E4M3) {
-    rep << "e4m3 path: the 3x3 always uses the 8 x 16 halo tiling; nothing to tune\n";
+    rep << "e4m3 path: the 3x3 always uses 8 x 16 halo tiles on CTA pairs; nothing to tune\n";
     return rep.str();
   }
   DeviceGuard g(m.device);
@@ -901,8 +907,8 @@ std::string UnifiedFPNCore::autotune(const void* const* in, void* const* out, vo
   if (iterations < 1) iterations = 1;
   for (int l = 3; l >= 0; --l) {
     float best_ms = -1.f;
-    int best_tw = m.tiling[l].halo ? 0 : m.tiling[l].tile_w;
-    for (int tw : {0, 8, 16, 32, 64, 128}) {  // 0 = halo reuse, 8 x 16 tiles
+    int best_tw = tiling_code(m.tiling[l]);
+    for (int tw : {-1, 0, 8, 16, 32, 64, 128}) {  // -1 / 0 = halo tiles on CTA pairs / single
       if (tw > 2 * m.W[l] && tw != 8) continue;  // wider than the image: pure padding
       const Conv3x3Tiling t = tiling_from_code(tw);
       TcPlan conv;
@@ -920,7 +926,8 @@ std::string UnifiedFPNCore::autotune(const void* const* in, void* const* out, vo
       cudaEventElapsedTime(&ms, m.prof[0], m.prof[1]);
       ms /= iterations;
       rep << "P" << (l + 2) << " 3x3 " << m.batch << "x" << m.H[l] << "x" << m.W[l] << " tile "
-          << t.tile_w << "x" << t.tile_h << (t.halo ? " halo" : "") << ": " << ms * 1e3
+          << t.tile_w << "x" << t.tile_h << (t.halo ? " halo" : "") << (t.pair ? " pair" : "")
+          << ": " << ms * 1e3
           << " us\n";
       if (best_ms < 0 || ms < best_ms) {
         best_ms = ms;
@@ -931,7 +938,7 @@ std::string UnifiedFPNCore::autotune(const void* const* in, void* const* out, vo
     m.tiling_tuned[l] = true;
     m.tuning_db[m.tuning_key(l)] = {best_tw, best_ms};
     rep << "P" << (l + 2) << " -> tile " << m.tiling[l].tile_w << "x" << m.tiling[l].tile_h
-        << (m.tiling[l].halo ? " halo" : "") << "\n";
+        << (m.tiling[l].halo ? " halo" : "") << (m.tiling[l].pair ? " pair" : "") << "\n";
   }
   m.release_graphs();
   if (device_status(true) != 0) FPN_THROW("device pipeline timeout during autotuning");
@@ -958,7 +965,8 @@ bool UnifiedFPNCore::load_tuning(const std::string& path) {
   int tw;
   float ms;
   while (f >> key >> tw >> ms) {
-    if (tw == 0 || (tw >= 8 && tw <= 128 && 128 % tw == 0)) impl_->tuning_db[key] = {tw, ms};
+    if (tw == -1 || tw == 0 || (tw >= 8 && tw <= 128 && 128 % tw == 0))
+      impl_->tuning_db[key] = {tw, ms};
   }
   Impl& m = *impl_;
   if (m.configured) {

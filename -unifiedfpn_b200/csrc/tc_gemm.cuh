@@ -273,12 +273,16 @@ __device__ __forceinline__ void tc_build_bilinear(uint8_t* a_stage, uint8_t* b_s
 // Epilogue role (warps 2..9) of the tensor-core kernels: per tile, TMEM -> registers,
 // + bias (+ global-memory bilinear taps on the lateral fallback path), convert,
 // 128-byte-swizzled staging tile, TMA tensor store; P6 rows for the top 3x3.
-template <int kMode, typename T>
+// kPair: the CTA is one half of a cta_group::2 pair; pair unit u covers tiles 2u (rank 0)
+// and 2u + 1 (rank 1; past the last tile it is a virtual, all-padding tile that is
+// computed but never stored), and each warp releases its accumulator on the pair
+// leader's barrier (shared::cluster address leader_acce).
+template <int kMode, typename T, bool kPair = false>
 __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtensorMap* map_out,
                                             uint32_t tmem_base, uint64_t* accf_bar,
                                             uint64_t* acce_bar, uint8_t* smem_stage,
                                             volatile int* abort_flag, int warp, int lane,
-                                            bool bil_mma) {
+                                            bool bil_mma, uint32_t leader_acce = 0) {
   using O = typename TcElem<T>::Out;
   constexpr bool kFp8 = TcElem<T>::kFp8;
   const int ew = warp - 2;
@@ -290,7 +294,13 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
   const bool taps_global = (kMode == 0) && args.coarse != nullptr && !bil_mma;
   int acc = 0;
   uint32_t acc_phase = 0;
-  for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x) {
+  const int rank = kPair ? static_cast<int>(cluster_ctarank()) : 0;
+  const int units = kPair ? (args.num_tiles + 1) / 2 : args.num_tiles;
+  const int ustep = kPair ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  for (int u = kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+       u < units; u += ustep) {
+    const int tile = kPair ? 2 * u + rank : u;
+    const bool real = tile < args.num_tiles;
     const bool ok =
         mbar_wait(&accf_bar[acc], acc_phase, abort_flag, args.status, kDevTimeoutEpilogue);
     if (!__all_sync(0xffffffffu, ok)) break;
@@ -300,8 +310,8 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
     tc_tile_origin(args, tile, n, x0, y0);
     const int py = y0 + row / tw;
     const int px = x0 + row % tw;
-    const bool valid = (py < args.H) && (px < args.W);
-    const float ascale = kFp8 ? __ldg(args.ascale + n * args.ascale_stride) : 1.f;
+    const bool valid = real && (py < args.H) && (px < args.W);
+    const float ascale = (kFp8 && real) ? __ldg(args.ascale + n * args.ascale_stride) : 1.f;
     uint32_t amax_bits = 0;  // max |stored value| of this thread in this tile (fp32 bits)
 
     // Fallback only: bilinear taps of the coarser merged map from global memory.
@@ -347,7 +357,12 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
         // All of this tile's accumulator columns for this warp are in registers:
         // hand the TMEM buffer back to the MMA warp before the memory work.
         tc_fence_before();
-        mbar_arrive(&acce_bar[acc]);
+        if constexpr (kPair) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(leader_acce + static_cast<uint32_t>(acc) * 8u);
+        } else {
+          mbar_arrive(&acce_bar[acc]);
+        }
       }
       float v[64];
       const float4* b4 = reinterpret_cast<const float4*>(args.bias + col0);
@@ -421,7 +436,7 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
       }
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) {
+      if (lane == 0 && real) {
         tma_store_4d(map_out, smem_stage + ew * kTcStagingPerWarp, col0, ox, oy, n);
         bulk_commit_group();
       }
@@ -429,7 +444,8 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
     if (args.amax_out != nullptr) {
       // One atomic per warp and tile at most, skipped once the image's maximum is larger.
       amax_bits = __reduce_max_sync(0xffffffffu, amax_bits);
-      if (lane == 0 && amax_bits > *reinterpret_cast<volatile unsigned*>(args.amax_out + n))
+      if (lane == 0 && real &&
+          amax_bits > *reinterpret_cast<volatile unsigned*>(args.amax_out + n))
         atomicMax(args.amax_out + n, amax_bits);
     }
     if (++acc == 2) {

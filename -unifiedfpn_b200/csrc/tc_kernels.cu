@@ -6,6 +6,7 @@
 #include <cstring>
 #include <mutex>
 
+#include "conv_pair.cuh"
 #include "kernels.h"
 #include "neck_kernel.cuh"
 #include "tc_gemm.cuh"
@@ -77,12 +78,14 @@ cudaError_t encode_nhwc(CUtensorMap* map, DType dt, const void* base, int N, int
   return encode(map, dt, 4, base, dims, strides, box);
 }
 
-// Weights [256][K] K-major, (one 128-byte row of K, 256) box.
-cudaError_t encode_weights(CUtensorMap* map, DType dt, const void* base, int K) {
+// Weights [256][K] K-major, (one 128-byte row of K, box_rows) box (256 rows, or 128 for
+// the half k-blocks of a CTA pair).
+cudaError_t encode_weights(CUtensorMap* map, DType dt, const void* base, int K,
+                           int box_rows = kTcBlockN) {
   const uint64_t esz = static_cast<uint64_t>(dtype_size(dt));
   uint64_t dims[2] = {static_cast<uint64_t>(K), kTcBlockN};
   uint64_t strides[1] = {static_cast<uint64_t>(K) * esz};
-  uint32_t box[2] = {static_cast<uint32_t>(128 / esz), kTcBlockN};
+  uint32_t box[2] = {static_cast<uint32_t>(128 / esz), static_cast<uint32_t>(box_rows)};
   return encode(map, dt, 2, base, dims, strides, box);
 }
 
@@ -163,6 +166,36 @@ cudaError_t launch_halo_t(const TcPlan& p, cudaStream_t s) {
   fpn_conv3x3_halo_kernel<T><<<p.grid, kTcThreads, HaloCfg::kSmemBytes, s>>>(
       p.map_a, p.map_b, p.map_out, a);
   return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_halo_pair_t(const TcPlan& p, cudaStream_t s) {
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(fpn_conv3x3_halo_pair_kernel<T>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         PairCfg::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  TcGemmArgs a;
+  std::memcpy(&a, p.args, sizeof(a));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(p.grid), 1, 1);
+  cfg.blockDim = dim3(kTcThreads, 1, 1);
+  cfg.dynamicSmemBytes = PairCfg::kSmemBytes;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, fpn_conv3x3_halo_pair_kernel<T>, p.map_a, p.map_b, p.map_out,
+                            a);
 }
 
 }  // namespace
@@ -294,22 +327,32 @@ cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w
   const bool halo = tiling.halo;
   if (halo && (tiling.tile_w != kHaloTileW || tiling.tile_h != kHaloTileH))
     return cudaErrorInvalidValue;
+  if (tiling.pair && !halo) return cudaErrorInvalidValue;
   // Halo path: one (tile_w + 2) x (tile_h + 2) box per channel block, origin (-1, -1).
   cudaError_t e = halo ? encode_nhwc(&plan.map_a, dt, x, N, H, W, C, kHaloTileW + 2,
                                      kHaloTileH + 2)
                        : encode_nhwc(&plan.map_a, dt, x, N, H, W, C, tiling.tile_w, tiling.tile_h);
   if (e != cudaSuccess) return e;
-  if ((e = encode_weights(&plan.map_b, dt, w, 9 * C)) != cudaSuccess) return e;
+  if ((e = encode_weights(&plan.map_b, dt, w, 9 * C, tiling.pair ? kTcBlockN / 2 : kTcBlockN)) !=
+      cudaSuccess)
+    return e;
   const int sw = tiling.tile_w < 32 ? tiling.tile_w : 32;
   if ((e = encode_nhwc(&plan.map_out, odt, out, N, H, W, kTcBlockN, sw, 32 / sw)) != cudaSuccess)
     return e;
   plan.map_coarse = plan.map_out;
   std::memcpy(plan.args, &a, sizeof(a));
-  plan.mode = halo ? 2 : 1;
+  plan.mode = tiling.pair ? 3 : (halo ? 2 : 1);
   plan.dtype = dt;
   plan.num_tiles = a.num_tiles;
   const int cap = max_ctas > 0 ? max_ctas : sm_count();
-  plan.grid = a.num_tiles < cap ? a.num_tiles : cap;
+  if (tiling.pair) {
+    // One (2,1,1) cluster per pair unit (two tiles), at most one CTA per SM.
+    const int units = (a.num_tiles + 1) / 2;
+    const int clusters = units < cap / 2 ? units : cap / 2;
+    plan.grid = 2 * (clusters > 0 ? clusters : 1);
+  } else {
+    plan.grid = a.num_tiles < cap ? a.num_tiles : cap;
+  }
   return cudaSuccess;
 }
 
@@ -476,7 +519,12 @@ cudaError_t launch_tc(const TcPlan& plan, cudaStream_t s) {
   if (plan.dtype == DType::E4M3) {
     if (plan.mode == 0) return launch_t<0, __nv_fp8_e4m3>(plan, s);
     if (plan.mode == 2) return launch_halo_t<__nv_fp8_e4m3>(plan, s);
+    if (plan.mode == 3) return launch_halo_pair_t<__nv_fp8_e4m3>(plan, s);
     return cudaErrorInvalidValue;
+  }
+  if (plan.mode == 3) {
+    return plan.dtype == DType::BF16 ? launch_halo_pair_t<__nv_bfloat16>(plan, s)
+                                     : launch_halo_pair_t<__half>(plan, s);
   }
   if (plan.mode == 0) {
     return plan.dtype == DType::BF16 ? launch_t<0, __nv_bfloat16>(plan, s)

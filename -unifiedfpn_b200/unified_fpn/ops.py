@@ -102,6 +102,7 @@ def fpn_conv3x3(input: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, p
     """3x3 pad-1 output conv (256 -> 256) + bias; with ``p6=True`` also returns
     P6 = max_pool2d(out, 1, 2).  ``weight`` is [256, 256, 3, 3] (any float dtype)
     or, for 16-bit inputs, already packed [256, 9, 256] by :func:`pack_conv3x3_weight`.
+    ``tile_w``: 0 = 8x16 halo tiles, -1 = halo tiles on CTA pairs, 8..128 = plain tiles.
     """
     _check_cuda(input, weight, bias)
     N, C, H, W = input.shape
@@ -272,7 +273,8 @@ def fpn_lateral_conv_fp8(input: torch.Tensor, input_scale, weight: torch.Tensor,
 
 
 def fpn_conv3x3_fp8(input: torch.Tensor, input_scale, weight: torch.Tensor,
-                    weight_scales: torch.Tensor, bias: torch.Tensor, p6: bool = False):
+                    weight_scales: torch.Tensor, bias: torch.Tensor, p6: bool = False,
+                    tile_w: int = 0):
     """FP8 3x3 pad-1 conv 256 -> 256 (+ optional P6): ``input`` e4m3 [N, 256, H, W];
     ``weight`` e4m3 packed [256, 9, 256] from :func:`quantize_fp8_rows` (pack3x3=True) with
     ``weight_scales`` [256]; ``input_scale`` 1 (per tensor) or N (per image) elements;
@@ -291,8 +293,8 @@ def fpn_conv3x3_fp8(input: torch.Tensor, input_scale, weight: torch.Tensor,
                       device=x.device, memory_format=torch.channels_last) if p6 else None
     check(lib.ufpn_conv3x3_e4m3(x.data_ptr(), xs.data_ptr(), per_img, weight.contiguous().data_ptr(),
                                 ws.data_ptr(), b.data_ptr(), out.data_ptr(),
-                                p6t.data_ptr() if p6t is not None else None, N, H, W, None,
-                                _stream(x)), "ufpn_conv3x3_e4m3")
+                                p6t.data_ptr() if p6t is not None else None, N, H, W, tile_w,
+                                None, _stream(x)), "ufpn_conv3x3_e4m3")
     return (out, p6t) if p6 else out
 
 

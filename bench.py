@@ -362,11 +362,11 @@ def main():
         if fp8:
             xq, xs = U.quantize_fp8(xr, per_image=True)
             wq, wsc = U.quantize_fp8_rows(w3, pack3x3=True)
-            conv = lambda: U.fpn_conv3x3_fp8(xq, xs, wq, wsc, bias)  # noqa: E731
+            conv = lambda: U.fpn_conv3x3_fp8(xq, xs, wq, wsc, bias, tile_w=-1)  # noqa: E731
         else:
             x = xr.to(dtype)
             wt = U.pack_conv3x3_weight(w3, dtype)
-            conv = lambda: U.fpn_conv3x3(x, wt, bias)  # noqa: E731
+            conv = lambda: U.fpn_conv3x3(x, wt, bias, tile_w=-1)  # noqa: E731
         reps = 20
         for _ in range(3):
             conv()
@@ -386,8 +386,9 @@ def main():
         peak = peaks["bf16_tflops"] * mult
         traffic = profile_traffic("conv3x3_fp8_p2_r50_640x640_b16" if fp8
                                   else "conv3x3_p2_r50_800x1216_b2")
-        roofline = {"kernel": f"conv3x3 P2 implicit GEMM (tcgen05 {'kind::f8f6f4' if fp8 else 'kind::f16'}),"
-                              f" {B}x{h2}x{w2}x256 -> 256",
+        # the engine's 3x3: 8x16 halo tiles on CTA pairs (tcgen05 cta_group::2)
+        roofline = {"kernel": f"conv3x3 P2 implicit GEMM (tcgen05 cta_group::2 "
+                              f"{'kind::f8f6f4' if fp8 else 'kind::f16'}), {B}x{h2}x{w2}x256 -> 256",
                     "bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
                     "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                     "peak_src": (f"derived: 2 x {peaks['src']} bf16 burst" if fp8

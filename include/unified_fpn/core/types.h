@@ -127,8 +127,8 @@ struct FPNTensor {
 };
 
 struct FPNKernelConfig {
-  // 3x3 conv: 0 = automatic (tuned tiling if any, else 8 x 16 tiles with halo reuse);
-  // 8..128 = plain tiles of that width (tile height = 128 / width).
+  // 3x3 conv: 0 = automatic (tuned tiling if any, else 8 x 16 tiles with halo reuse on
+  // CTA pairs); 8..128 = plain tiles of that width (tile height = 128 / width).
   int tile_size = 0;
   int channels_per_thread = 8;   // accepted for API compatibility
   int shared_mem_size = 0;       // accepted for API compatibility

@@ -83,6 +83,9 @@ struct Conv3x3Tiling {
   // 3x3 only: 8 x 16 tiles whose (18 x 10) halo is loaded once per 64-channel block
   // and shared by the nine taps (instead of one shifted box per tap).
   bool halo = false;
+  // Halo tiles on CTA pairs (tcgen05 cta_group::2, M = 256 per MMA): each CTA streams
+  // half of every weight k-block.
+  bool pair = false;
 };
 // The 3x3 default: halo reuse with 8 x 16 tiles.
 inline Conv3x3Tiling halo_tiling() {
@@ -90,6 +93,11 @@ inline Conv3x3Tiling halo_tiling() {
   t.tile_w = 8;
   t.tile_h = 16;
   t.halo = true;
+  return t;
+}
+inline Conv3x3Tiling halo_pair_tiling() {
+  Conv3x3Tiling t = halo_tiling();
+  t.pair = true;
   return t;
 }
 
@@ -102,7 +110,7 @@ struct TcPlan {
   alignas(64) CUtensorMap map_out;
   alignas(64) CUtensorMap map_coarse;
   unsigned char args[256];  // TcGemmArgs, opaque outside tc_kernels.cu
-  int mode = 0;             // 0 lateral, 1 conv3x3, 2 conv3x3 with halo reuse
+  int mode = 0;             // 0 lateral, 1 conv3x3, 2 conv3x3 halo, 3 conv3x3 halo on CTA pairs
   DType dtype = DType::BF16;
   int grid = 0;
   int num_tiles = 0;

@@ -121,7 +121,9 @@ int ufpn_lateral_conv(int dtype, int layout, const void* x, const void* w, const
  *   dtype F16/BF16: NHWC x, w in dtype packed [256][9][256] (ufpn_pack_conv3x3_weights).
  *   dtype F32: NCHW x, w fp32 [256][256][3][3].
  * tile_w: 0 = 8 x 16 tiles with halo reuse (default: each 64-channel halo is loaded once
- * and shared by the nine taps); 8..128 = plain tiles of that width (one box per tap). */
+ * and shared by the nine taps); -1 = the same tiles on CTA pairs (tcgen05 cta_group::2:
+ * two SMs share one M = 256 MMA stream and each streams half of the weights); 8..128 =
+ * plain tiles of that width (one box per tap). */
 int ufpn_conv3x3(int dtype, const void* x, const void* w, const float* bias, void* out,
                  void* p6, int N, int H, int W, int tile_w, void* stream);
 
@@ -201,13 +203,14 @@ int ufpn_lateral_conv_e4m3(const void* x, const float* x_scale, int x_scale_per_
                            const void* w, const float* w_scales, const float* bias,
                            const void* coarse, void* out, int N, int Cin, int H, int W, int Hc,
                            int Wc, unsigned* amax_out, void* stream);
-/* FP8 3x3 pad-1 conv 256 -> 256 (8 x 16 halo tiles), NHWC: x e4m3 [N][H][W][256] with device
+/* FP8 3x3 pad-1 conv 256 -> 256 (8 x 16 halo tiles; tile_w -1: on CTA pairs, as for
+ * ufpn_conv3x3), NHWC: x e4m3 [N][H][W][256] with device
  * scale(s) as above; w e4m3 packed [256][9][256] (ufpn_quantize_e4m3_rows with pack_cin =
  * 256) with scales [256]; out (and optional p6 = out[::2, ::2]) bf16; amax_out as above.
  * Same role as launch_output_conv (fpn_engine.cu:315-362). */
 int ufpn_conv3x3_e4m3(const void* x, const float* x_scale, int x_scale_per_image, const void* w,
                       const float* w_scales, const float* bias, void* out, void* p6, int N,
-                      int H, int W, unsigned* amax_out, void* stream);
+                      int H, int W, int tile_w, unsigned* amax_out, void* stream);
 /* fpn_engine.cu:191-245 (forward) for an engine configured with dtype UFPN_DTYPE_E4M3
  * (NHWC): inputs C2..C5 e4m3, input_scales[l] = device fp32 per-tensor scale of inputs[l];
  * outputs P2..P5 (and p6) bf16.  Each merged map M_l is quantised per image before its 3x3,

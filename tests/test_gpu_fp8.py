@@ -127,8 +127,11 @@ def test_conv3x3_fp8_matches_oracle(cuda_device, shape, per_image):
     qwd, swd = U.quantize_fp8_rows(w3.cuda(), pack3x3=True)
     out, p6 = U.fpn_conv3x3_fp8(_cl(_upload_codes(qm)), torch.from_numpy(sm), qwd, swd, b.cuda(),
                                 p6=True)
+    out2, p62 = U.fpn_conv3x3_fp8(_cl(_upload_codes(qm)), torch.from_numpy(sm), qwd, swd, b.cuda(),
+                                  p6=True, tile_w=-1)   # the same tiles on CTA pairs
     torch.cuda.synchronize()
     assert U.device_status() == 0
+    assert torch.equal(out, out2) and torch.equal(p6, p62)
     acc = torch.nn.functional.conv2d(torch.from_numpy(qm).double(), torch.from_numpy(qw).double(),
                                      padding=1)
     cs = (torch.from_numpy(sm).reshape(-1, 1) * torch.from_numpy(sw).reshape(1, -1)).double()

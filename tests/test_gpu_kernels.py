@@ -189,6 +189,32 @@ def test_conv3x3_tc_with_p6(cuda_device, dtype, shape):
     assert torch.equal(p6.cpu(), y.cpu()[:, :, ::2, ::2])
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", [(1, 16, 8), (1, 13, 21), (2, 25, 38), (3, 17, 5), (1, 1, 1),
+                                   (2, 200, 304)])
+def test_conv3x3_cta_pair_equals_single(cuda_device, dtype, shape):
+    """Halo tiles on CTA pairs (tcgen05 cta_group::2, M = 256: two tiles per MMA stream, each
+    CTA streaming half of the weights) give bitwise the results of single-CTA halo tiles:
+    every output's K summation runs in the same order.  Odd tile counts exercise the
+    virtual (never stored) second tile of the last pair; (2, 200, 304) is the R50 P2 map."""
+    import unified_fpn as U
+    n, h, w_ = shape
+    g = torch.Generator().manual_seed(h * 31 + w_)
+    x = torch.randn(n, 256, h, w_, generator=g).to(dtype)
+    w = torch.randn(256, 256, 3, 3, generator=g) * (2.0 / 2304) ** 0.5
+    b = torch.rand(256, generator=g) * 0.2 - 0.1
+    xd = _cl(x.to(cuda_device))
+    wp = U.pack_conv3x3_weight(w.to(cuda_device), dtype)
+    y1, p1 = U.fpn_conv3x3(xd, wp, b.to(cuda_device), p6=True, tile_w=0)
+    y2, p2 = U.fpn_conv3x3(xd, wp, b.to(cuda_device), p6=True, tile_w=-1)
+    torch.cuda.synchronize()
+    assert U.device_status() == 0
+    assert torch.equal(y1, y2) and torch.equal(p1, p2)
+    if n * h * w_ <= 4096:
+        ref = O.conv3x3(x.float(), w.to(dtype).float(), b)
+        assert O.rel_err(y2.cpu(), ref) < BF16_TOL
+
+
 def test_conv3x3_fp32(cuda_device):
     import unified_fpn as U
     g = torch.Generator().manual_seed(3)
