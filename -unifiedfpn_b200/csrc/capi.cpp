@@ -213,9 +213,12 @@ int ufpn_core_get_neck_trace(const ufpn_core* core, unsigned long long* out8) {
 
 int ufpn_core_set_schedule(ufpn_core* core, int fused_neck_kernel) {
   if (!core) return fail(UFPN_ERR_INVALID_ARG, "NULL core");
+  if (fused_neck_kernel < 0 || fused_neck_kernel > 2)
+    return fail(UFPN_ERR_INVALID_ARG, "schedule: 0 split (two streams), 1 fused, 2 split on one stream");
   return guarded([&] {
     FPNKernelConfig c = core->core.get_kernel_config();
-    c.fused_neck_kernel = fused_neck_kernel != 0;
+    c.fused_neck_kernel = fused_neck_kernel == 1;
+    c.single_stream = fused_neck_kernel == 2;
     core->core.set_kernel_config(c);
     return UFPN_OK;
   });

@@ -354,8 +354,9 @@ struct UnifiedFPNCore::Impl {
       }
       return launches;
     }
-    cudaStream_t conv_stream = prof_events ? main : side;
-    if (!prof_events) {
+    const bool one_stream = prof_events || cfg.single_stream;
+    cudaStream_t conv_stream = one_stream ? main : side;
+    if (!one_stream) {
       check(cudaEventRecord(ev_fork, main), "event");
       check(cudaStreamWaitEvent(side, ev_fork, 0), "event");
     }
@@ -382,7 +383,7 @@ struct UnifiedFPNCore::Impl {
       lv[l].conv_tiling = tiling_for(l);
     }
     auto conv_level = [&](int l) {
-      if (!prof_events) {
+      if (!one_stream) {
         check(cudaEventRecord(ev_lat[l], main), "event");
         check(cudaStreamWaitEvent(side, ev_lat[l], 0), "event");
       }
@@ -428,7 +429,7 @@ struct UnifiedFPNCore::Impl {
                                   ((H[3] - 1) / 2 + 1) * ((W[3] - 1) / 2 + 1), false, conv_stream),
            "NHWC->NCHW");
     }
-    if (!prof_events) {
+    if (!one_stream) {
       check(cudaEventRecord(ev_join, side), "event");
       check(cudaStreamWaitEvent(main, ev_join, 0), "event");
     }
@@ -449,11 +450,12 @@ struct UnifiedFPNCore::Impl {
       check(e, what);
       ++launches;
     };
-    const cudaStream_t conv_stream = prof_events ? main : side;
+    const bool one_stream = prof_events || cfg.single_stream;
+    const cudaStream_t conv_stream = one_stream ? main : side;
     if (prof_events) cudaEventRecord(prof[0], main);
     check(cudaMemsetAsync(fp8_amax, 0, 4 * static_cast<size_t>(batch) * sizeof(unsigned), main),
           "memset");
-    if (!prof_events) {
+    if (!one_stream) {
       check(cudaEventRecord(ev_fork, main), "event");
       check(cudaStreamWaitEvent(side, ev_fork, 0), "event");
       for (int i = 0; i < 2; ++i) check(cudaStreamWaitEvent(lat_side[i], ev_fork, 0), "event");
@@ -473,7 +475,7 @@ struct UnifiedFPNCore::Impl {
       ok(ufpn::launch_tc(p, st), "e4m3 lateral launch");
     };
     auto conv_level = [&](int l) {
-      if (!prof_events) {
+      if (!one_stream) {
         check(cudaEventRecord(ev_lat[l], main), "event");
         check(cudaStreamWaitEvent(side, ev_lat[l], 0), "event");
       }
@@ -498,15 +500,15 @@ struct UnifiedFPNCore::Impl {
     // their own streams so the small P5 grid shares the machine with the larger ones.
     lateral(3, nullptr, fp8_amax + 3 * batch, main);
     for (int i = 0; i < 2; ++i) {
-      const cudaStream_t st = prof_events ? main : lat_side[i];
+      const cudaStream_t st = one_stream ? main : lat_side[i];
       lateral(2 - i, nullptr, nullptr, st);
-      if (!prof_events) check(cudaEventRecord(ev_lat_done[i], st), "event");
+      if (!one_stream) check(cudaEventRecord(ev_lat_done[i], st), "event");
     }
     if (prof_events) cudaEventRecord(prof[1], main);
     conv_level(3);
     if (prof_events) cudaEventRecord(prof[2], main);
     for (int l = 2; l >= 1; --l) {
-      if (!prof_events) check(cudaStreamWaitEvent(main, ev_lat_done[2 - l], 0), "event");
+      if (!one_stream) check(cudaStreamWaitEvent(main, ev_lat_done[2 - l], 0), "event");
       // M3 also gets its copy pre-divided by the P2 lateral's per-channel scale, which the P2
       // lateral adds through its tensor-core top-down k-block.
       ufpn::MergeScaledCopy m3s;
@@ -525,7 +527,7 @@ struct UnifiedFPNCore::Impl {
     if (prof_events) cudaEventRecord(prof[7], main);
     conv_level(0);
     if (prof_events) cudaEventRecord(prof[8], main);
-    if (!prof_events) {
+    if (!one_stream) {
       check(cudaEventRecord(ev_join, side), "event");
       check(cudaStreamWaitEvent(main, ev_join, 0), "event");
     }

@@ -284,10 +284,12 @@ class UnifiedFPN:
         check(lib.ufpn_core_set_kernel_config(self._h, tile_size, channels_per_thread, int(use_tensor_cores),
                                               _ACT[activation], int(enable_graph_capture)), "set_kernel_config")
 
-    def set_schedule(self, fused_neck_kernel: bool = False) -> None:
-        """Tensor-core schedule: one persistent kernel for the whole neck, or eight
-        per-level kernels on two streams (default).  Results are bitwise identical."""
-        check(lib.ufpn_core_set_schedule(self._h, int(fused_neck_kernel)), "set_schedule")
+    def set_schedule(self, fused_neck_kernel: bool = False, single_stream: bool = False) -> None:
+        """Tensor-core schedule: one persistent kernel for the whole neck, or per-level
+        kernels on two streams (default) or, with ``single_stream``, one after the other on
+        the caller's stream (bitwise the same results as the default)."""
+        mode = 1 if fused_neck_kernel else (2 if single_stream else 0)
+        check(lib.ufpn_core_set_schedule(self._h, mode), "set_schedule")
 
     def neck_timeline(self, backbone_features) -> dict:
         """Runs one forward with the fused neck kernel's device timeline recorded and

@@ -220,8 +220,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-roofline", action="store_true")
-    ap.add_argument("--schedule", choices=["fused", "split"], default="split",
-                    help="one persistent neck kernel, or eight per-level kernels on two streams")
+    ap.add_argument("--schedule", choices=["fused", "split", "serial"], default="split",
+                    help="one persistent neck kernel, per-level kernels on two streams, or the "
+                         "per-level kernels one after the other on one stream")
     args = ap.parse_args()
     fp8 = args.dtype == "e4m3"
     if args.batch is None:
@@ -272,7 +273,7 @@ def main():
             scales.append(None)
     in_mb = sum(B * c * h * w * esz for c, (h, w) in zip(R50_CHANNELS, sizes)) / 1e6
     fpn = U.UnifiedFPN(device=dev)
-    fpn.set_schedule(fused_neck_kernel=args.schedule == "fused")
+    fpn.set_schedule(fused_neck_kernel=args.schedule == "fused", single_stream=args.schedule == "serial")
     outs = []
     for s in range(n_sets):
         o = fpn(feats[s], return_p6=True, input_scales=scales[s])

@@ -140,6 +140,9 @@ struct FPNKernelConfig {
   // device-side level dependencies (true), or as 8 kernels on two streams (false, the
   // faster schedule at the R50 800x1216 batch-2 workload today).
   bool fused_neck_kernel = false;
+  // Split schedule only: run every kernel on the caller's stream, one after the other
+  // (false: each level's 3x3 on a second stream, overlapping the top-down chain).
+  bool single_stream = false;
 };
 
 struct FPNWeights {

@@ -77,9 +77,10 @@ int ufpn_core_forward(ufpn_core* core, const void* const* inputs, void* const* o
  * FPNActivation ordinal (only NONE is supported). */
 int ufpn_core_set_kernel_config(ufpn_core* core, int tile_size, int channels_per_thread,
                                 int use_tensor_cores, int activation, int enable_graph_capture);
-/* Tensor-core schedule: 1 = one persistent kernel for the whole neck, 0 = eight kernels on
- * two streams (default).  No reference counterpart (its engine launched 16 kernels on four
- * unordered streams, fpn_engine.cu:191-245). */
+/* Tensor-core schedule: 1 = one persistent kernel for the whole neck, 0 = per-level kernels
+ * on two streams (default), 2 = the same kernels one after the other on the caller's stream.
+ * No reference counterpart (its engine launched 16 kernels on four unordered streams,
+ * fpn_engine.cu:191-245). */
 int ufpn_core_set_schedule(ufpn_core* core, int fused_neck_kernel);
 /* fpn_engine.cu:408-415 (get_memory_usage) */
 size_t ufpn_core_get_memory_usage(const ufpn_core* core);

@@ -210,3 +210,24 @@ def test_host_pipeline_matches_forward(cuda_device, fp8):
     for e, o in zip(expect, outs):
         for a, b in zip(e, o):
             assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("fp8", [False, True])
+def test_single_stream_schedule_is_bitwise_equal(cuda_device, fp8):
+    """The split schedule's kernels run one after the other on one stream give exactly the
+    two-stream results."""
+    import unified_fpn as U
+    chans, sizes = O.R50_CHANNELS, O.level_sizes(160, 224)
+    fs = [_cl(f.cuda()) for f in O.make_features(2, chans, sizes, seed=61, dist="normal")]
+    if fp8:
+        qs = [U.quantize_fp8(f) for f in fs]
+        feats, sc = [q for q, _ in qs], torch.cat([s for _, s in qs])
+    else:
+        feats, sc = [f.to(torch.bfloat16) for f in fs], None
+    fpn = U.UnifiedFPN()
+    two = _run(fpn, feats, input_scales=sc)
+    fpn.set_schedule(single_stream=True)
+    one = _run(fpn, feats, input_scales=sc)
+    assert fpn.device_status() == 0
+    for a, b in zip(two, one):
+        assert torch.equal(a, b)
