@@ -474,15 +474,17 @@ struct UnifiedFPNCore::Impl {
             "plan e4m3 lateral");
       ok(ufpn::launch_tc(p, st), "e4m3 lateral launch");
     };
-    auto conv_level = [&](int l) {
+    // quantise = false: qmerged[l] and its scales were written by the kernel producing M_l.
+    auto conv_level = [&](int l, bool quantise = true) {
       if (!one_stream) {
         check(cudaEventRecord(ev_lat[l], main), "event");
         check(cudaStreamWaitEvent(side, ev_lat[l], 0), "event");
       }
       const long long n = static_cast<long long>(batch) * H[l] * W[l] * cout;
-      ok(ufpn::launch_quantize_e4m3(DType::BF16, merged[l], n, batch, fp8_amax + l * batch,
-                                    qmerged[l], fp8_scale + l * batch, conv_stream),
-         "quantise merged map");
+      if (quantise)
+        ok(ufpn::launch_quantize_e4m3(DType::BF16, merged[l], n, batch, fp8_amax + l * batch,
+                                      qmerged[l], fp8_scale + l * batch, conv_stream),
+           "quantise merged map");
       ufpn::TcScales sc;
       sc.ascale = fp8_scale + l * batch;
       sc.ascale_per_image = true;

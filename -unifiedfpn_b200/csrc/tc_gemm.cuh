@@ -127,6 +127,12 @@ struct TcGemmArgs {
   // optional: amax_out[n] = atomicMax of |out| (fp32 bits) over image n's stored elements
   // (the absmax a following per-image e4m3 quantisation of this output needs)
   unsigned* amax_out;
+  // 0: store the 16-bit output; 1: store nothing (only amax_out); 2: store the output
+  // quantised to e4m3 per image with the absmax in qamax[n] (the 16-bit value rounded
+  // first, then e4m3(x * 448 / amax)), writing the dequantisation scales to qscale_out[n]
+  int out_mode;
+  const unsigned* qamax;
+  float* qscale_out;
 };
 
 template <typename T>
@@ -163,6 +169,18 @@ struct Pack<__half> {
     return *reinterpret_cast<uint16_t*>(&v);
   }
 };
+
+__device__ __forceinline__ void st_shared_v2(uint32_t addr, uint32_t x, uint32_t y) {
+  asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(addr), "r"(x), "r"(y) : "memory");
+}
+// Four floats scaled by `inv` to four e4m3 bytes (nearest even, saturated), low byte first.
+__device__ __forceinline__ uint32_t tc_e4m3x4(float a, float b, float c, float d, float inv) {
+  const uint32_t lo =
+      __nv_cvt_float2_to_fp8x2(make_float2(a * inv, b * inv), __NV_SATFINITE, __NV_E4M3);
+  const uint32_t hi =
+      __nv_cvt_float2_to_fp8x2(make_float2(c * inv, d * inv), __NV_SATFINITE, __NV_E4M3);
+  return lo | (hi << 16);
+}
 
 __device__ __forceinline__ void tc_tile_origin(const TcGemmArgs& a, int tile, int& n, int& x0,
                                                int& y0) {
@@ -313,6 +331,13 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
     const bool valid = real && (py < args.H) && (px < args.W);
     const float ascale = (kFp8 && real) ? __ldg(args.ascale + n * args.ascale_stride) : 1.f;
     uint32_t amax_bits = 0;  // max |stored value| of this thread in this tile (fp32 bits)
+    const int omode = args.out_mode;
+    float qinv = 1.f;
+    if (omode == 2 && real) {
+      const float qa = __uint_as_float(__ldg(args.qamax + n));
+      qinv = qa > 0.f ? __fdiv_rn(448.f, qa) : 1.f;
+      if (ew == 0 && lane == 0) args.qscale_out[n] = qa > 0.f ? __fdiv_rn(qa, 448.f) : 1.f;
+    }
 
     // Fallback only: bilinear taps of the coarser merged map from global memory.
     TcTaps tp{};
@@ -410,8 +435,9 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
           }
         }
       }
-      // The previous TMA store from this warp's staging buffer must have read it.
-      if (lane == 0) bulk_wait_group_read<0>();
+      // The previous TMA store from this warp's staging buffer must have read it (the e4m3
+      // row of a tile is assembled from both steps, so it is only waited for at step 0).
+      if (lane == 0 && (omode == 0 || (omode == 2 && step == 0))) bulk_wait_group_read<0>();
       __syncwarp();
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -430,15 +456,30 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
             amax_bits = max(amax_bits, max(__float_as_uint(f.x), __float_as_uint(f.y)));
           }
         }
-        st_shared_v4(stage_addr + lane * 128 + ((j ^ (lane & 7)) << 4), o);
-        if (emit_p6)
-          reinterpret_cast<uint4*>(p6_row + static_cast<size_t>(col0) * sizeof(O))[j] = o;
+        if (omode == 0) {
+          st_shared_v4(stage_addr + lane * 128 + ((j ^ (lane & 7)) << 4), o);
+          if (emit_p6)
+            reinterpret_cast<uint4*>(p6_row + static_cast<size_t>(col0) * sizeof(O))[j] = o;
+        } else if (omode == 2) {
+          // 8 channels -> 8 e4m3 bytes, half of 16-byte chunk (step * 4 + j / 2) of the row
+          const float2 f0 = Pack<O>::unpack(o.x), f1 = Pack<O>::unpack(o.y);
+          const float2 f2 = Pack<O>::unpack(o.z), f3 = Pack<O>::unpack(o.w);
+          const uint32_t q0 = tc_e4m3x4(f0.x, f0.y, f1.x, f1.y, qinv);
+          const uint32_t q1 = tc_e4m3x4(f2.x, f2.y, f3.x, f3.y, qinv);
+          const int chunk = step * 4 + (j >> 1);
+          st_shared_v2(stage_addr + lane * 128 + ((chunk ^ (lane & 7)) << 4) + (j & 1) * 8, q0,
+                       q1);
+        }
       }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0 && real) {
-        tma_store_4d(map_out, smem_stage + ew * kTcStagingPerWarp, col0, ox, oy, n);
-        bulk_commit_group();
+      if (omode == 0 || (omode == 2 && step == 1)) {
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && real) {
+          // e4m3: the warp's 128 channels (128 bytes per pixel) in one store
+          tma_store_4d(map_out, smem_stage + ew * kTcStagingPerWarp,
+                       omode == 0 ? col0 : chalf * 128, ox, oy, n);
+          bulk_commit_group();
+        }
       }
     }
     if (args.amax_out != nullptr) {

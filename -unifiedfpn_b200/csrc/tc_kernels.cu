@@ -241,6 +241,9 @@ cudaError_t plan_tc_lateral(TcPlan& plan, DType dt, const void* x, const void* w
   if (!valid_tiling(tiling)) return cudaErrorInvalidValue;
   if (coarse && (Hc <= 0 || Wc <= 0)) return cudaErrorInvalidValue;
   if (fp8 && (!sc.ascale || !sc.wscale)) return cudaErrorInvalidValue;
+  if (sc.out_mode < 0 || sc.out_mode > 2 || (sc.out_mode == 1 && !sc.amax_out) ||
+      (sc.out_mode == 2 && (!sc.qamax || !sc.qscale_out)))
+    return cudaErrorInvalidValue;
   if (!aligned16(out) || (coarse && !aligned16(coarse)) || !aligned16(bias) ||
       (fp8 && !aligned16(sc.wscale)))
     return cudaErrorMisalignedAddress;
@@ -258,11 +261,15 @@ cudaError_t plan_tc_lateral(TcPlan& plan, DType dt, const void* x, const void* w
   a.ascale_stride = sc.ascale_per_image ? 1 : 0;
   a.wscale = sc.wscale;
   a.amax_out = sc.amax_out;
+  a.out_mode = sc.out_mode;
+  a.qamax = sc.qamax;
+  a.qscale_out = sc.qscale_out;
   cudaError_t e = encode_nhwc(&plan.map_a, dt, x, N, H, W, Cin, tiling.tile_w, tiling.tile_h);
   if (e != cudaSuccess) return e;
   if ((e = encode_weights(&plan.map_b, dt, w, Cin)) != cudaSuccess) return e;
   const int sw = tiling.tile_w < 32 ? tiling.tile_w : 32;
-  if ((e = encode_nhwc(&plan.map_out, odt, out, N, H, W, kTcBlockN, sw, 32 / sw)) != cudaSuccess)
+  if ((e = encode_nhwc(&plan.map_out, sc.out_mode == 2 ? DType::E4M3 : odt, out, N, H, W,
+                       kTcBlockN, sw, 32 / sw)) != cudaSuccess)
     return e;
   plan.map_coarse = plan.map_out;  // unused unless a coarse map is staged
   if (coarse) {

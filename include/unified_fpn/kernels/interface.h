@@ -129,6 +129,13 @@ struct TcScales {
   // wscale[c]) per channel (MergeScaledCopy), so the top-down add can run as a tensor-core
   // k-block on the unscaled accumulator.  Otherwise the epilogue adds it from global memory.
   bool coarse_prescaled = false;
+  // Lateral output: 0 = store the 16-bit map; 1 = store nothing (amax_out only); 2 = store
+  // it quantised to e4m3 per image with the absmax in qamax[n] (out is then e4m3), writing
+  // the dequantisation scales to qscale_out[n].  1 then 2 = a two-pass lateral whose
+  // quantised output equals quantising the stored 16-bit map.
+  int out_mode = 0;
+  const unsigned* qamax = nullptr;
+  float* qscale_out = nullptr;
 };
 
 // Lateral 1x1 (+ optional fused bilinear upsample-add of the coarser merged map).
