@@ -104,6 +104,7 @@ struct UnifiedFPNCore::Impl {
   void* merged[4] = {};   // M_l in the compute dtype (bf16 for e4m3 inputs)
   void* qmerged[4] = {};  // e4m3: M_l quantised per image (input of the 3x3)
   void* m3_scaled = nullptr;  // e4m3: M3 / (scale(C2) * lateral-P2 weight scale), per channel
+  void* wb_table = nullptr;   // P2 lateral's precomputed top-down (bilinear) weights
   const float* in_scale[4] = {};  // e4m3: scales of the current forward's inputs
   unsigned* fp8_amax = nullptr;   // e4m3: [4][N] per-image absmax of M_l (fp32 bits)
   float* fp8_scale = nullptr;     // e4m3: [4][N] per-image dequantisation scale of M_l
@@ -163,6 +164,8 @@ struct UnifiedFPNCore::Impl {
     fp8_scale = nullptr;
     cudaFree(m3_scaled);
     m3_scaled = nullptr;
+    cudaFree(wb_table);
+    wb_table = nullptr;
     workspace_bytes = 0;
   }
   void free_weights() {
@@ -415,6 +418,7 @@ struct UnifiedFPNCore::Impl {
                                 batch, cin[0], H[0], W[0], H[1], W[1], lv[0].lat_tiling, d_status,
                                 0),
           "plan lateral");
+    ufpn::tc_attach_wb_table(lat2, wb_table);
     ok(ufpn::launch_tc(lat2, main), "lateral launch");
     if (prof_events) cudaEventRecord(prof[7], main);
     conv_level(0);
@@ -472,6 +476,7 @@ struct UnifiedFPNCore::Impl {
                                   coarse ? W[l + 1] : 0, ufpn::default_tiling(H[l], W[l]),
                                   d_status, 0, sc),
             "plan e4m3 lateral");
+      if (l == 0) ufpn::tc_attach_wb_table(p, wb_table);
       ok(ufpn::launch_tc(p, st), "e4m3 lateral launch");
     };
     // quantise = false: qmerged[l] and its scales were written by the kernel producing M_l.
@@ -642,6 +647,19 @@ void UnifiedFPNCore::configure_levels(const std::vector<FPNDimensions>& dims, in
       m.check(cudaMalloc(&m.nhwc_in[l], px * m.cin[l] * esz), "workspace");
       m.check(cudaMalloc(&m.nhwc_out[l], px * m.cout * esz), "workspace");
       total += px * (m.cin[l] + m.cout) * esz;
+    }
+  }
+  if (m.tensor_core_path()) {
+    // The P2 lateral's top-down weights depend only on the geometry: build them once.
+    const Conv3x3Tiling lt = ufpn::default_tiling(m.H[0], m.W[0]);
+    const size_t tb = ufpn::tc_wb_table_bytes(m.H[0], m.W[0], m.H[1], m.W[1], lt);
+    if (tb > 0) {
+      m.check(cudaMalloc(&m.wb_table, tb), "workspace");
+      m.check(ufpn::tc_build_wb_table(dt, m.H[0], m.W[0], m.H[1], m.W[1], lt, m.wb_table,
+                                      m.setup),
+              "build bilinear weight table");
+      m.check(cudaStreamSynchronize(m.setup), "build bilinear weight table");
+      total += tb;
     }
   }
   if (dt == DType::E4M3) {

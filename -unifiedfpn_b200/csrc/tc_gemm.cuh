@@ -56,14 +56,6 @@ constexpr int kTcStagingPerWarp = 32 * 128;  // 32 rows x 64 channels (bf16/fp16
 constexpr int kTcCoarseMaxPix = 64;          // coarse-box pixels = one MMA k-block
 constexpr int kTcStages = 4;
 
-struct TcCfg {
-  static constexpr int kStages = kTcStages;
-  static constexpr int kOffB = kStages * kTcAStage;
-  static constexpr int kOffStaging = kOffB + kStages * kTcBStage;
-  static constexpr int kOffBars = kOffStaging + kTcEpiWarps * kTcStagingPerWarp;
-  static constexpr int kSmemBytes = kOffBars + 256 + 1024 /*alignment slack*/;
-};
-static_assert(TcCfg::kSmemBytes <= 232448, "tc smem");
 
 // Operand element traits.  A k-block is one 128-byte swizzled row of channels:
 // 64 channels of a 16-bit type, 128 of e4m3.  Either way a k-block is 4 MMAs of
@@ -94,6 +86,30 @@ struct TcElem<__nv_fp8_e4m3> {
 template <typename T>
 constexpr int kKbElems = 128 / static_cast<int>(sizeof(T));  // channels per k-block
 constexpr int kMmaPerKb = 4;                                   // 32-byte K steps per k-block
+
+// Shared-memory and warp plan of fpn_tc_gemm_kernel: kStages operand stages, kEpiWarps
+// epilogue warps with kStageBufs staging buffers each.  The e4m3 lateral (mode 0) has a
+// 2-k-block loop per tile, so its time per tile is the epilogue's latency chain (TMEM ->
+// registers -> scale -> bf16 -> staging -> TMA store) rather than the MMAs: it runs 16
+// epilogue warps, each owning 64 of the 256 output channels, and pays for their staging
+// with one operand stage.  (Measured per tile: 16-bit laterals, with 4 k-blocks, are
+// faster with 8 epilogue warps and 4 stages.)
+template <int kMode, typename T>
+struct TcCfgT {
+  static constexpr bool kWide = kMode == 0 && TcElem<T>::kFp8;
+  static constexpr int kEpiWarps = kWide ? 16 : kTcEpiWarps;
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;
+  static constexpr int kStages = kWide ? 3 : kTcStages;
+  static constexpr int kStageBufs = 1;
+  static constexpr int kOffB = kStages * kTcAStage;
+  static constexpr int kOffStaging = kOffB + kStages * kTcBStage;
+  static constexpr int kOffBars = kOffStaging + kStageBufs * kEpiWarps * kTcStagingPerWarp;
+  static constexpr int kSmemBytes = kOffBars + 256 + 1024 /*alignment slack*/;
+};
+static_assert(TcCfgT<0, __nv_fp8_e4m3>::kSmemBytes <= 232448 &&
+                  TcCfgT<0, __nv_bfloat16>::kSmemBytes <= 232448 &&
+                  TcCfgT<1, __nv_bfloat16>::kSmemBytes <= 232448,
+              "tc smem");
 
 template <typename T>
 __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
@@ -133,6 +149,9 @@ struct TcGemmArgs {
   int out_mode;
   const unsigned* qamax;
   float* qscale_out;
+  // lateral top-down k-block: precomputed Wb table (tc_wb_table_kernel), or null to build
+  // Wb per tile in the producer warp
+  const uint8_t* wb_table;
 };
 
 template <typename T>
@@ -239,28 +258,36 @@ __device__ __forceinline__ TcTaps tc_taps(int py, int px, int H, int W, int Hc, 
   return t;
 }
 
-// Whole-warp builder of the bilinear operands of one tile, written with generic
+// Bilinear operands of one tile's top-down k-block, written by a whole warp with generic
 // stores (the caller fences the async proxy afterwards):
-//   a_stage: Wb, 128 rows (tile pixels) x 64 k (box pixels), K-major 128-byte swizzle;
-//   b_stage: zeroes the box rows k >= cbox_w * cbox_h of the 4 MN-major 64-channel
-//            blocks (TMA fills rows below that) so no stale bits meet a zero weight.
-template <typename T>
-__device__ __forceinline__ void tc_build_bilinear(uint8_t* a_stage, uint8_t* b_stage, int lane,
-                                                  int x0, int y0, int tile_w, int H, int W,
-                                                  int Hc, int Wc, float scale_y, float scale_x,
-                                                  int cbox_w, int cbox_h) {
-  const uint32_t a_addr = smem_u32(a_stage);
+//   tc_build_wb:    Wb, 128 rows (tile pixels) x 64 k (box pixels), K-major 128-byte
+//                   swizzle relative to a 1024-byte-aligned base (so the same bytes, stored
+//                   in global memory, form a table a bulk copy can bring back unchanged);
+//   tc_zero_btail:  zeroes the box rows k >= cbox_w * cbox_h of the nb MN-major 64-channel
+//                   blocks of the B stage (TMA fills rows below that), so no stale bits
+//                   meet a zero weight.
+__device__ __forceinline__ void tc_zero_btail(uint8_t* b_stage, int lane, int kbox, int nb) {
   const uint32_t b_addr = smem_u32(b_stage);
   const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-  for (int i = lane; i < kTcAStage / 16; i += 32) st_shared_v4(a_addr + i * 16, z);
-  const int kbox = cbox_w * cbox_h;
-  for (int i = lane; i < 4 * (kTcCoarseMaxPix - kbox) * 8; i += 32) {
-    const int blk = i / ((kTcCoarseMaxPix - kbox) * 8);
-    const int rem = i - blk * ((kTcCoarseMaxPix - kbox) * 8);
+  const int per = (kTcCoarseMaxPix - kbox) * 8;  // 16-byte chunks per block
+  for (int i = lane; i < nb * per; i += 32) {
+    const int blk = i / per;
+    const int rem = i - blk * per;
     const int row = kbox + (rem >> 3);
     st_shared_v4(b_addr + blk * (kTcCoarseMaxPix * 128) + row * 128 + (rem & 7) * 16, z);
   }
+}
+
+template <typename T>
+__device__ __forceinline__ void tc_build_wb(uint8_t* a_stage, int lane, int x0, int y0,
+                                            int tile_w, int H, int W, int Hc, int Wc,
+                                            float scale_y, float scale_x, int cbox_w,
+                                            int cbox_h) {
+  const uint32_t a_addr = smem_u32(a_stage);
+  const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+  for (int i = lane; i < kTcAStage / 16; i += 32) st_shared_v4(a_addr + i * 16, z);
   __syncwarp();
+  const int kbox = cbox_w * cbox_h;
   const int cy0 = static_cast<int>(tc_src(y0, scale_y, Hc));
   const int cx0 = static_cast<int>(tc_src(x0, scale_x, Wc));
 #pragma unroll 1
@@ -288,14 +315,40 @@ __device__ __forceinline__ void tc_build_bilinear(uint8_t* a_stage, uint8_t* b_s
   }
 }
 
-// Epilogue role (warps 2..9) of the tensor-core kernels: per tile, TMEM -> registers,
+template <typename T>
+__device__ __forceinline__ void tc_build_bilinear(uint8_t* a_stage, uint8_t* b_stage, int lane,
+                                                  int x0, int y0, int tile_w, int H, int W,
+                                                  int Hc, int Wc, float scale_y, float scale_x,
+                                                  int cbox_w, int cbox_h) {
+  tc_zero_btail(b_stage, lane, cbox_w * cbox_h, 4);
+  tc_build_wb<T>(a_stage, lane, x0, y0, tile_w, H, W, Hc, Wc, scale_y, scale_x, cbox_w, cbox_h);
+}
+
+// Precomputed Wb table: entry ty * tiles_x + tx holds the 16 KB Wb of tile (tx, ty) (the
+// same for every image).  One 32-thread block per entry.
+template <typename T>
+__global__ void __launch_bounds__(32) tc_wb_table_kernel(const TcGemmArgs a, uint8_t* table) {
+  extern __shared__ uint8_t wb_raw[];
+  uint8_t* buf = wb_raw + ((1024u - (smem_u32(wb_raw) & 1023u)) & 1023u);
+  const int e = blockIdx.x;
+  const int tx = e % a.tiles_x, ty = e / a.tiles_x;
+  tc_build_wb<T>(buf, threadIdx.x, tx * a.tile_w, ty * a.tile_h, a.tile_w, a.H, a.W, a.Hc, a.Wc,
+                 a.scale_y, a.scale_x, a.cbox_w, a.cbox_h);
+  __syncwarp();
+  const uint4* src = reinterpret_cast<const uint4*>(buf);
+  uint4* dst = reinterpret_cast<uint4*>(table + static_cast<size_t>(e) * kTcAStage);
+  for (int i = threadIdx.x; i < kTcAStage / 16; i += 32) dst[i] = src[i];
+}
+
+// Epilogue role (warps 2 .. 2 + kEpiW - 1) of the tensor-core kernels: per tile, TMEM -> registers,
 // + bias (+ global-memory bilinear taps on the lateral fallback path), convert,
 // 128-byte-swizzled staging tile, TMA tensor store; P6 rows for the top 3x3.
 // kPair: the CTA is one half of a cta_group::2 pair; pair unit u covers tiles 2u (rank 0)
 // and 2u + 1 (rank 1; past the last tile it is a virtual, all-padding tile that is
 // computed but never stored), and each warp releases its accumulator on the pair
 // leader's barrier (shared::cluster address leader_acce).
-template <int kMode, typename T, bool kPair = false>
+template <int kMode, typename T, bool kPair = false, int kStageBufs = 1,
+          int kEpiW = kTcEpiWarps>
 __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtensorMap* map_out,
                                             uint32_t tmem_base, uint64_t* accf_bar,
                                             uint64_t* acce_bar, uint8_t* smem_stage,
@@ -303,12 +356,19 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
                                             bool bil_mma, uint32_t leader_acce = 0) {
   using O = typename TcElem<T>::Out;
   constexpr bool kFp8 = TcElem<T>::kFp8;
+  // kEpiW / 4 warps share each TMEM lane quarter; each owns kChans output channels,
+  // processed in 64-channel steps.
+  constexpr int kChans = kTcBlockN / (kEpiW / 4);
+  constexpr int kSteps = kChans / 64;
+  static_assert(kEpiW % 4 == 0 && kChans % 64 == 0, "epilogue warp split");
   const int ew = warp - 2;
-  const int quarter = warp & 3;  // TMEM lanes 32*quarter..+31
-  const int chalf = ew >> 2;     // output channels chalf*128 .. +127
+  const int quarter = warp & 3;  // TMEM lanes 32*quarter..+31 (hardware: warp id % 4)
+  const int chalf = ew >> 2;     // output channels chalf*kChans .. +kChans-1
   const int row = quarter * 32 + lane;
   const int tw = args.tile_w;
-  const uint32_t stage_addr = smem_u32(smem_stage + ew * kTcStagingPerWarp);
+  // Staging buffers of this warp: kStageBufs x (32 rows x 128 bytes), used round robin.
+  uint8_t* const my_stage = smem_stage + ew * kStageBufs * kTcStagingPerWarp;
+  int sbuf = 0;
   const bool taps_global = (kMode == 0) && args.coarse != nullptr && !bil_mma;
   int acc = 0;
   uint32_t acc_phase = 0;
@@ -369,117 +429,128 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
     const int oy = y0 + wrow0 / tw;
 
 #pragma unroll 1
-    for (int step = 0; step < 2; ++step) {
-      const int col0 = chalf * 128 + step * 64;
-      uint32_t r[64];
-      __syncwarp();
+    for (int step = 0; step < kSteps; ++step) {
+      const int col0 = chalf * kChans + step * 64;
       const uint32_t taddr = tmem_base + static_cast<uint32_t>(acc * kTcBlockN + col0) +
                              (static_cast<uint32_t>(quarter * 32) << 16);
-      tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-      tmem_ld32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-      tmem_wait_ld();
-      if (step == 1) {
-        // All of this tile's accumulator columns for this warp are in registers:
-        // hand the TMEM buffer back to the MMA warp before the memory work.
-        tc_fence_before();
-        if constexpr (kPair) {
-          __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(leader_acce + static_cast<uint32_t>(acc) * 8u);
-        } else {
-          mbar_arrive(&acce_bar[acc]);
-        }
-      }
-      float v[64];
-      const float4* b4 = reinterpret_cast<const float4*>(args.bias + col0);
-      if constexpr (kFp8) {
-        const float4* s4 = reinterpret_cast<const float4*>(args.wscale + col0);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float4 bb = __ldg(b4 + i);
-          const float4 ss = __ldg(s4 + i);
-          v[4 * i + 0] = fmaf(__uint_as_float(r[4 * i + 0]), ascale * ss.x, bb.x);
-          v[4 * i + 1] = fmaf(__uint_as_float(r[4 * i + 1]), ascale * ss.y, bb.y);
-          v[4 * i + 2] = fmaf(__uint_as_float(r[4 * i + 2]), ascale * ss.z, bb.z);
-          v[4 * i + 3] = fmaf(__uint_as_float(r[4 * i + 3]), ascale * ss.w, bb.w);
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float4 bb = __ldg(b4 + i);
-          v[4 * i + 0] = __uint_as_float(r[4 * i + 0]) + bb.x;
-          v[4 * i + 1] = __uint_as_float(r[4 * i + 1]) + bb.y;
-          v[4 * i + 2] = __uint_as_float(r[4 * i + 2]) + bb.z;
-          v[4 * i + 3] = __uint_as_float(r[4 * i + 3]) + bb.w;
-        }
-      }
-      if (taps_global) {
-        const size_t off = static_cast<size_t>(col0) * sizeof(O);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint4 a = __ldg(reinterpret_cast<const uint4*>(g00 + off) + j);
-          const uint4 b = __ldg(reinterpret_cast<const uint4*>(g01 + off) + j);
-          const uint4 c = __ldg(reinterpret_cast<const uint4*>(g10 + off) + j);
-          const uint4 d = __ldg(reinterpret_cast<const uint4*>(g11 + off) + j);
-          const uint32_t au[4] = {a.x, a.y, a.z, a.w};
-          const uint32_t bu[4] = {b.x, b.y, b.z, b.w};
-          const uint32_t cu[4] = {c.x, c.y, c.z, c.w};
-          const uint32_t du[4] = {d.x, d.y, d.z, d.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 fa = Pack<O>::unpack(au[e]);
-            const float2 fb = Pack<O>::unpack(bu[e]);
-            const float2 fc = Pack<O>::unpack(cu[e]);
-            const float2 fd = Pack<O>::unpack(du[e]);
-            v[8 * j + 2 * e + 0] += tp.w00 * fa.x + tp.w01 * fb.x + tp.w10 * fc.x + tp.w11 * fd.x;
-            v[8 * j + 2 * e + 1] += tp.w00 * fa.y + tp.w01 * fb.y + tp.w10 * fc.y + tp.w11 * fd.y;
-          }
-        }
-      }
-      // The previous TMA store from this warp's staging buffer must have read it (the e4m3
+      // The TMA store that last read this staging buffer must be done with it (the e4m3
       // row of a tile is assembled from both steps, so it is only waited for at step 0).
-      if (lane == 0 && (omode == 0 || (omode == 2 && step == 0))) bulk_wait_group_read<0>();
-      __syncwarp();
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        uint4 o;
-        o.x = Pack<O>::pack(v[8 * j + 0], v[8 * j + 1]);
-        o.y = Pack<O>::pack(v[8 * j + 2], v[8 * j + 3]);
-        o.z = Pack<O>::pack(v[8 * j + 4], v[8 * j + 5]);
-        o.w = Pack<O>::pack(v[8 * j + 6], v[8 * j + 7]);
-        if (args.amax_out != nullptr && valid) {
-          // max |x| of the rounded 16-bit values: clear the sign bits, then compare as
-          // unsigned (order-preserving for non-negative floats of one format).
-          const uint32_t w4[4] = {o.x, o.y, o.z, o.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = Pack<O>::unpack(w4[e] & 0x7FFF7FFFu);
-            amax_bits = max(amax_bits, max(__float_as_uint(f.x), __float_as_uint(f.y)));
+      if (omode == 0 || (omode == 2 && step == 0)) {
+        if (lane == 0) bulk_wait_group_read<kStageBufs - 1>();
+      }
+      const uint32_t stage_addr = smem_u32(my_stage + sbuf * kTcStagingPerWarp);
+      // Two 32-column halves per 64-channel step (half the live registers).
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        const int c0 = col0 + half * 32;
+        uint32_t r[32];
+        __syncwarp();
+        tmem_ld32(taddr + half * 32, r);
+        tmem_wait_ld();
+        if (step == kSteps - 1 && half == 1) {
+          // All of this tile's accumulator columns for this warp are in registers:
+          // hand the TMEM buffer back to the MMA warp before the memory work.
+          tc_fence_before();
+          if constexpr (kPair) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(leader_acce + static_cast<uint32_t>(acc) * 8u);
+          } else {
+            mbar_arrive(&acce_bar[acc]);
           }
         }
-        if (omode == 0) {
-          st_shared_v4(stage_addr + lane * 128 + ((j ^ (lane & 7)) << 4), o);
-          if (emit_p6)
-            reinterpret_cast<uint4*>(p6_row + static_cast<size_t>(col0) * sizeof(O))[j] = o;
-        } else if (omode == 2) {
-          // 8 channels -> 8 e4m3 bytes, half of 16-byte chunk (step * 4 + j / 2) of the row
-          const float2 f0 = Pack<O>::unpack(o.x), f1 = Pack<O>::unpack(o.y);
-          const float2 f2 = Pack<O>::unpack(o.z), f3 = Pack<O>::unpack(o.w);
-          const uint32_t q0 = tc_e4m3x4(f0.x, f0.y, f1.x, f1.y, qinv);
-          const uint32_t q1 = tc_e4m3x4(f2.x, f2.y, f3.x, f3.y, qinv);
-          const int chunk = step * 4 + (j >> 1);
-          st_shared_v2(stage_addr + lane * 128 + ((chunk ^ (lane & 7)) << 4) + (j & 1) * 8, q0,
-                       q1);
+        float v[32];
+        const float4* b4 = reinterpret_cast<const float4*>(args.bias + c0);
+        if constexpr (kFp8) {
+          const float4* s4 = reinterpret_cast<const float4*>(args.wscale + c0);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 bb = __ldg(b4 + i);
+            const float4 ss = __ldg(s4 + i);
+            v[4 * i + 0] = fmaf(__uint_as_float(r[4 * i + 0]), ascale * ss.x, bb.x);
+            v[4 * i + 1] = fmaf(__uint_as_float(r[4 * i + 1]), ascale * ss.y, bb.y);
+            v[4 * i + 2] = fmaf(__uint_as_float(r[4 * i + 2]), ascale * ss.z, bb.z);
+            v[4 * i + 3] = fmaf(__uint_as_float(r[4 * i + 3]), ascale * ss.w, bb.w);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 bb = __ldg(b4 + i);
+            v[4 * i + 0] = __uint_as_float(r[4 * i + 0]) + bb.x;
+            v[4 * i + 1] = __uint_as_float(r[4 * i + 1]) + bb.y;
+            v[4 * i + 2] = __uint_as_float(r[4 * i + 2]) + bb.z;
+            v[4 * i + 3] = __uint_as_float(r[4 * i + 3]) + bb.w;
+          }
+        }
+        if (taps_global) {
+          const size_t off = static_cast<size_t>(c0) * sizeof(O);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 a = __ldg(reinterpret_cast<const uint4*>(g00 + off) + j);
+            const uint4 b = __ldg(reinterpret_cast<const uint4*>(g01 + off) + j);
+            const uint4 c = __ldg(reinterpret_cast<const uint4*>(g10 + off) + j);
+            const uint4 d = __ldg(reinterpret_cast<const uint4*>(g11 + off) + j);
+            const uint32_t au[4] = {a.x, a.y, a.z, a.w};
+            const uint32_t bu[4] = {b.x, b.y, b.z, b.w};
+            const uint32_t cu[4] = {c.x, c.y, c.z, c.w};
+            const uint32_t du[4] = {d.x, d.y, d.z, d.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 fa = Pack<O>::unpack(au[e]);
+              const float2 fb = Pack<O>::unpack(bu[e]);
+              const float2 fc = Pack<O>::unpack(cu[e]);
+              const float2 fd = Pack<O>::unpack(du[e]);
+              v[8 * j + 2 * e + 0] += tp.w00 * fa.x + tp.w01 * fb.x + tp.w10 * fc.x + tp.w11 * fd.x;
+              v[8 * j + 2 * e + 1] += tp.w00 * fa.y + tp.w01 * fb.y + tp.w10 * fc.y + tp.w11 * fd.y;
+            }
+          }
+        }
+        __syncwarp();
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const int j = half * 4 + jj;  // 16-byte chunk of the 128-byte staging row
+          uint4 o;
+          o.x = Pack<O>::pack(v[8 * jj + 0], v[8 * jj + 1]);
+          o.y = Pack<O>::pack(v[8 * jj + 2], v[8 * jj + 3]);
+          o.z = Pack<O>::pack(v[8 * jj + 4], v[8 * jj + 5]);
+          o.w = Pack<O>::pack(v[8 * jj + 6], v[8 * jj + 7]);
+          if (args.amax_out != nullptr && valid) {
+            // max |x| of the rounded 16-bit values: clear the sign bits, then compare as
+            // unsigned (order-preserving for non-negative floats of one format).
+            const uint32_t w4[4] = {o.x, o.y, o.z, o.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = Pack<O>::unpack(w4[e] & 0x7FFF7FFFu);
+              amax_bits = max(amax_bits, max(__float_as_uint(f.x), __float_as_uint(f.y)));
+            }
+          }
+          if (omode == 0) {
+            st_shared_v4(stage_addr + lane * 128 + ((j ^ (lane & 7)) << 4), o);
+            if (emit_p6)
+              reinterpret_cast<uint4*>(p6_row + static_cast<size_t>(col0) * sizeof(O))[j] = o;
+          } else if (kSteps == 2 && omode == 2) {
+            // 8 channels -> 8 e4m3 bytes, half of 16-byte chunk (step * 4 + j / 2) of the row
+            const float2 f0 = Pack<O>::unpack(o.x), f1 = Pack<O>::unpack(o.y);
+            const float2 f2 = Pack<O>::unpack(o.z), f3 = Pack<O>::unpack(o.w);
+            const uint32_t q0 = tc_e4m3x4(f0.x, f0.y, f1.x, f1.y, qinv);
+            const uint32_t q1 = tc_e4m3x4(f2.x, f2.y, f3.x, f3.y, qinv);
+            const int chunk = step * 4 + (j >> 1);
+            st_shared_v2(stage_addr + lane * 128 + ((chunk ^ (lane & 7)) << 4) + (j & 1) * 8,
+                         q0, q1);
+          }
         }
       }
-      if (omode == 0 || (omode == 2 && step == 1)) {
+      if (omode == 0 || (omode == 2 && step == kSteps - 1)) {
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0 && real) {
-          // e4m3: the warp's 128 channels (128 bytes per pixel) in one store
-          tma_store_4d(map_out, smem_stage + ew * kTcStagingPerWarp,
-                       omode == 0 ? col0 : chalf * 128, ox, oy, n);
+        if (lane == 0) {
+          // e4m3: the warp's 128 channels (128 bytes per pixel) in one store.  Every buffer
+          // use commits a group (empty for virtual tiles) so group counts stay in step.
+          if (real)
+            tma_store_4d(map_out, my_stage + sbuf * kTcStagingPerWarp,
+                         omode == 0 ? col0 : chalf * 128, ox, oy, n);
           bulk_commit_group();
         }
+        if (++sbuf == kStageBufs) sbuf = 0;
       }
     }
     if (args.amax_out != nullptr) {
@@ -499,19 +570,20 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
 }
 
 template <int kMode, typename T>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(TcCfgT<kMode, T>::kThreads, 1)
     fpn_tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
                        const __grid_constant__ CUtensorMap map_b,
                        const __grid_constant__ CUtensorMap map_out,
                        const __grid_constant__ CUtensorMap map_coarse, const TcGemmArgs args) {
-  constexpr int S = TcCfg::kStages;
+  using Cfg = TcCfgT<kMode, T>;
+  constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint8_t* smem_a = smem;
-  uint8_t* smem_b = smem + TcCfg::kOffB;
-  uint8_t* smem_stage = smem + TcCfg::kOffStaging;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TcCfg::kOffBars);
+  uint8_t* smem_b = smem + Cfg::kOffB;
+  uint8_t* smem_stage = smem + Cfg::kOffStaging;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBars);
   uint64_t* full_bar = bars;
   uint64_t* empty_bar = bars + S;
   uint64_t* accf_bar = bars + 2 * S;
@@ -534,7 +606,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accf_bar[b], 1);
-      mbar_init(&acce_bar[b], kTcEpiWarps * 32);
+      mbar_init(&acce_bar[b], Cfg::kEpiWarps * 32);
     }
     mbar_init(done_bar, 1);
     *abort_flag = 0;
@@ -588,17 +660,31 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         kPolicyEvictLast);
           }
         } else {
-          // Bilinear k-block: Wb into the A stage (generic stores, whole warp), the
-          // coarse box into the B stage (TMA), then one arrival with the TMA bytes.
-          tc_build_bilinear<typename TcElem<T>::Out>(smem_a + stage * kTcAStage, smem_b + stage * kTcBStage, lane,
-                               x0, y0, args.tile_w, args.H, args.W, args.Hc, args.Wc,
-                               args.scale_y, args.scale_x, args.cbox_w, args.cbox_h);
+          // Bilinear k-block: Wb into the A stage (a bulk copy of the tile's precomputed
+          // table entry, else generic stores by the whole warp), the coarse box into the
+          // B stage (TMA), then one arrival with the async bytes.
+          if (args.wb_table != nullptr)
+            tc_zero_btail(smem_b + stage * kTcBStage, lane, args.cbox_w * args.cbox_h, 4);
+          else
+            tc_build_bilinear<typename TcElem<T>::Out>(
+                smem_a + stage * kTcAStage, smem_b + stage * kTcBStage, lane, x0, y0,
+                args.tile_w, args.H, args.W, args.Hc, args.Wc, args.scale_y, args.scale_x,
+                args.cbox_w, args.cbox_h);
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
             const int cy = static_cast<int>(tc_src(y0, args.scale_y, args.Hc));
             const int cx = static_cast<int>(tc_src(x0, args.scale_x, args.Wc));
-            mbar_arrive_expect_tx(&full_bar[stage], coarse_bytes);
+            if (args.wb_table != nullptr) {
+              mbar_arrive_expect_tx(&full_bar[stage], coarse_bytes + kTcAStage);
+              const int e = (tile % args.tiles_x) + ((tile / args.tiles_x) % args.tiles_y) *
+                                                       args.tiles_x;
+              bulk_load(smem_a + stage * kTcAStage,
+                        args.wb_table + static_cast<size_t>(e) * kTcAStage, kTcAStage,
+                        &full_bar[stage]);
+            } else {
+              mbar_arrive_expect_tx(&full_bar[stage], coarse_bytes);
+            }
             for (int b = 0; b < 4; ++b)
               tma_load_4d(smem_b + stage * kTcBStage + b * (kTcCoarseMaxPix * 128), &map_coarse,
                           &full_bar[stage], b * 64, cx, cy, n, kPolicyEvictLast);
@@ -684,7 +770,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    tc_epilogue<kMode, T>(args, &map_out, tmem_base, accf_bar, acce_bar, smem_stage,
+    tc_epilogue<kMode, T, false, Cfg::kStageBufs, Cfg::kEpiWarps>(args, &map_out, tmem_base, accf_bar, acce_bar, smem_stage,
                           abort_flag, warp, lane, bil_mma);
   }
 

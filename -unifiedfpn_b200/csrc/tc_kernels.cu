@@ -138,13 +138,13 @@ cudaError_t launch_t(const TcPlan& p, cudaStream_t s) {
   if (dev < 64 && !configured[dev]) {
     cudaError_t e = cudaFuncSetAttribute(fpn_tc_gemm_kernel<kMode, T>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         TcCfg::kSmemBytes);
+                                         TcCfgT<kMode, T>::kSmemBytes);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
   TcGemmArgs a;
   std::memcpy(&a, p.args, sizeof(a));
-  fpn_tc_gemm_kernel<kMode, T><<<p.grid, kTcThreads, TcCfg::kSmemBytes, s>>>(
+  fpn_tc_gemm_kernel<kMode, T><<<p.grid, TcCfgT<kMode, T>::kThreads, TcCfgT<kMode, T>::kSmemBytes, s>>>(
       p.map_a, p.map_b, p.map_out, p.map_coarse, a);
   return cudaGetLastError();
 }
@@ -241,8 +241,9 @@ cudaError_t plan_tc_lateral(TcPlan& plan, DType dt, const void* x, const void* w
   if (!valid_tiling(tiling)) return cudaErrorInvalidValue;
   if (coarse && (Hc <= 0 || Wc <= 0)) return cudaErrorInvalidValue;
   if (fp8 && (!sc.ascale || !sc.wscale)) return cudaErrorInvalidValue;
-  if (sc.out_mode < 0 || sc.out_mode > 2 || (sc.out_mode == 1 && !sc.amax_out) ||
-      (sc.out_mode == 2 && (!sc.qamax || !sc.qscale_out)))
+  // (out_mode 2 assembles 128-byte e4m3 rows from two 64-channel steps per warp; the
+  // lateral's 16 epilogue warps own 64 channels each, so it is not available here.)
+  if (sc.out_mode < 0 || sc.out_mode > 1 || (sc.out_mode == 1 && !sc.amax_out))
     return cudaErrorInvalidValue;
   if (!aligned16(out) || (coarse && !aligned16(coarse)) || !aligned16(bias) ||
       (fp8 && !aligned16(sc.wscale)))
@@ -361,6 +362,49 @@ cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w
     plan.grid = a.num_tiles < cap ? a.num_tiles : cap;
   }
   return cudaSuccess;
+}
+
+size_t tc_wb_table_bytes(int H, int W, int Hc, int Wc, Conv3x3Tiling t) {
+  if (!valid_tiling(t) || H <= 0 || W <= 0 || Hc <= 0 || Wc <= 0) return 0;
+  const float sy = static_cast<float>(Hc) / static_cast<float>(H);
+  const float sx = static_cast<float>(Wc) / static_cast<float>(W);
+  const int ch = coarse_span(H, t.tile_h, sy, Hc);
+  const int cw = coarse_span(W, t.tile_w, sx, Wc);
+  if (ch * cw > kTcCoarseMaxPix) return 0;  // the lateral adds taps in its epilogue instead
+  const size_t entries = static_cast<size_t>((W + t.tile_w - 1) / t.tile_w) *
+                         static_cast<size_t>((H + t.tile_h - 1) / t.tile_h);
+  return entries * kTcAStage;
+}
+
+cudaError_t tc_build_wb_table(DType dt, int H, int W, int Hc, int Wc, Conv3x3Tiling t,
+                              void* table, cudaStream_t s) {
+  const size_t bytes = tc_wb_table_bytes(H, W, Hc, Wc, t);
+  if (bytes == 0 || !table || !aligned16(table)) return cudaErrorInvalidValue;
+  TcGemmArgs a;
+  std::memset(&a, 0, sizeof(a));
+  fill_tiling(a, 1, H, W, t);
+  a.Hc = Hc;
+  a.Wc = Wc;
+  a.scale_y = static_cast<float>(Hc) / static_cast<float>(H);
+  a.scale_x = static_cast<float>(Wc) / static_cast<float>(W);
+  a.cbox_h = coarse_span(H, t.tile_h, a.scale_y, Hc);
+  a.cbox_w = coarse_span(W, t.tile_w, a.scale_x, Wc);
+  const int entries = a.tiles_x * a.tiles_y;
+  const size_t smem = kTcAStage + 1024;
+  if (dt == DType::F16)
+    tc_wb_table_kernel<__half><<<entries, 32, smem, s>>>(a, static_cast<uint8_t*>(table));
+  else
+    tc_wb_table_kernel<__nv_bfloat16><<<entries, 32, smem, s>>>(a, static_cast<uint8_t*>(table));
+  return cudaGetLastError();
+}
+
+bool tc_attach_wb_table(TcPlan& plan, const void* table) {
+  TcGemmArgs a;
+  std::memcpy(&a, plan.args, sizeof(a));
+  if (plan.mode != 0 || !a.coarse || a.cbox_w <= 0 || !table) return false;
+  a.wb_table = static_cast<const uint8_t*>(table);
+  std::memcpy(plan.args, &a, sizeof(a));
+  return true;
 }
 
 static_assert(sizeof(NeckParams) <= sizeof(NeckPlan::params), "NeckPlan::params too small");

@@ -151,6 +151,16 @@ cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w
                             const float* bias, void* out, void* p6, int N, int H, int W,
                             Conv3x3Tiling tiling, int* status, int max_ctas,
                             const TcScales& scales = TcScales());
+// Precomputed bilinear-weight table of the lateral's tensor-core top-down add (one 16 KB
+// entry per tile position of an H x W map upsampled from Hc x Wc with tiling t; the same
+// for every image).  Bytes needed (0 when that lateral adds the taps in its epilogue),
+// building it (dt: the lateral's input dtype), and attaching it to a lateral plan (false
+// if the plan has no tensor-core top-down add).  A plan without a table builds its weights
+// per tile in the producer warp.
+size_t tc_wb_table_bytes(int H, int W, int Hc, int Wc, Conv3x3Tiling t);
+cudaError_t tc_build_wb_table(DType dt, int H, int W, int Hc, int Wc, Conv3x3Tiling t,
+                              void* table, cudaStream_t s);
+bool tc_attach_wb_table(TcPlan& plan, const void* table);
 // Tiling with the fewest padded pixels for an H x W map (ties: 16 wide).
 Conv3x3Tiling default_tiling(int H, int W);
 
