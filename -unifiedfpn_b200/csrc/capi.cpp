@@ -509,6 +509,26 @@ int ufpn_conv3x3_e4m3(const void* x, const float* x_scale, int x_scale_per_image
   return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "e4m3 conv3x3 launch");
 }
 
+int ufpn_conv3x3_e4m3_from_bf16(const void* x, const unsigned* amax_bits, const void* w,
+                                const float* w_scales, const float* bias, void* out, void* p6,
+                                int N, int H, int W, void* stream) {
+  if (!x || !amax_bits || !w || !w_scales || !bias || !out)
+    return fail(UFPN_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (N <= 0 || H <= 0 || W <= 0) return fail(UFPN_ERR_INVALID_ARG, "sizes must be positive");
+  if (!ufpn::aligned16(x) || !ufpn::aligned16(w) || !ufpn::aligned16(out) ||
+      !ufpn::aligned16(bias) || !ufpn::aligned16(w_scales) || (p6 && !ufpn::aligned16(p6)))
+    return fail(UFPN_ERR_ALIGNMENT, "tensors must be 16-byte aligned");
+  ufpn::TcScales sc;
+  sc.wscale = w_scales;
+  sc.in_amax = amax_bits;
+  ufpn::TcPlan plan;
+  cudaError_t e = ufpn::plan_tc_conv3x3(plan, DType::E4M3, x, w, bias, out, p6, N, H, W,
+                                        ufpn::halo_pair_tiling(), device_status_word(), 0, sc);
+  if (e != cudaSuccess) return cuda_fail(e, "plan e4m3 conv3x3");
+  e = ufpn::launch_tc(plan, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "e4m3 conv3x3 launch");
+}
+
 // ------------------------------------------------------------------ reference C ABI
 namespace {
 

@@ -17,6 +17,13 @@
 //   acce[a]            leader's; 16 warp arrivals (8 epilogue warps per CTA)
 // A cluster barrier after initialisation and another before TMEM is released keep either
 // CTA from touching the other's shared memory or TMEM outside their lifetimes.
+//
+// kCvt (e4m3 only): the input is the bf16 merged map and its per-image absmax; each CTA's
+// producer brings the bf16 halo (two 64-channel boxes) into a raw buffer (rfull / rempty,
+// local), and 4 converter warps quantise it into the e4m3 halo buffer exactly as the
+// standalone quantiser does (e4m3(x * 448 / amax[n]), nearest even, saturated), then arrive
+// on the leader's hfull (8 arrivals: 4 warps x 2 CTAs).  No separate quantise pass and no
+// e4m3 copy of the map in HBM.
 #pragma once
 
 #include "tc_gemm.cuh"
@@ -24,14 +31,20 @@
 namespace ufpn {
 
 constexpr int kPairBStage = (kTcBlockN / 2) * 128;  // half of a weight k-block: 16 KB
-constexpr int kPairStages = 8;
-struct PairCfg {
-  static constexpr int kOffHalo = kPairStages * kPairBStage;
-  static constexpr int kOffStaging = kOffHalo + kHaloBufs * kHaloBytes;
+constexpr int kPairCvtWarps = 4;
+template <bool kCvt>
+struct PairCfgT {
+  static constexpr int kStages = kCvt ? 6 : 8;
+  static constexpr int kThreads = kTcThreads + (kCvt ? 32 * kPairCvtWarps : 0);
+  static constexpr int kOffHalo = kStages * kPairBStage;
+  static constexpr int kOffRaw = kOffHalo + kHaloBufs * kHaloBytes;  // kCvt: 2 bf16 boxes
+  static constexpr int kOffStaging = kOffRaw + (kCvt ? 2 * kHaloBytes : 0);
   static constexpr int kOffBars = kOffStaging + kTcEpiWarps * kTcStagingPerWarp;
   static constexpr int kSmemBytes = kOffBars + 512 + 1024;
 };
-static_assert(PairCfg::kSmemBytes <= 232448, "pair smem");
+using PairCfg = PairCfgT<false>;
+static_assert(PairCfgT<false>::kSmemBytes <= 232448 && PairCfgT<true>::kSmemBytes <= 232448,
+              "pair smem");
 
 template <typename T>
 __device__ __forceinline__ void tc_mma_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
@@ -49,21 +62,24 @@ __device__ __forceinline__ void pair_settle_ns(uint64_t ns) {
   }
 }
 
-template <typename T>
-__global__ void __launch_bounds__(kTcThreads, 1)
+template <typename T, bool kCvt = false>
+__global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
     fpn_conv3x3_halo_pair_kernel(const __grid_constant__ CUtensorMap map_a,
                                  const __grid_constant__ CUtensorMap map_b,
                                  const __grid_constant__ CUtensorMap map_out,
                                  const TcGemmArgs args) {
-  constexpr int S = kPairStages;
+  static_assert(!kCvt || TcElem<T>::kFp8, "the converter quantises to e4m3");
+  using Cfg = PairCfgT<kCvt>;
+  constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   // Both CTAs compute the same aligned offset (same dynamic shared memory layout).
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint8_t* smem_b = smem;
-  uint8_t* smem_halo = smem + PairCfg::kOffHalo;
-  uint8_t* smem_stage = smem + PairCfg::kOffStaging;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + PairCfg::kOffBars);
+  uint8_t* smem_halo = smem + Cfg::kOffHalo;
+  uint8_t* smem_rawbuf = smem + Cfg::kOffRaw;
+  uint8_t* smem_stage = smem + Cfg::kOffStaging;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBars);
   uint64_t* full_bar = bars;
   uint64_t* empty_bar = bars + S;
   uint64_t* hfull_bar = bars + 2 * S;
@@ -71,7 +87,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* accf_bar = hempty_bar + kHaloBufs;
   uint64_t* acce_bar = accf_bar + 2;
   uint64_t* done_bar = acce_bar + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+  uint64_t* rfull_bar = done_bar + 1;   // kCvt
+  uint64_t* rempty_bar = rfull_bar + 1;  // kCvt
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rempty_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -89,7 +107,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&empty_bar[s], 1);
     }
     for (int h = 0; h < kHaloBufs; ++h) {
-      mbar_init(&hfull_bar[h], 1);
+      mbar_init(&hfull_bar[h], kCvt ? 2 * kPairCvtWarps : 1);
       mbar_init(&hempty_bar[h], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -97,6 +115,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&acce_bar[b], 2 * kTcEpiWarps);
     }
     mbar_init(done_bar, 1);
+    mbar_init(rfull_bar, 1);
+    mbar_init(rempty_bar, kPairCvtWarps);
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tmap(&map_a);
@@ -121,21 +141,36 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const uint32_t full0 = mapa_shared(smem_u32(full_bar), 0);
       const uint32_t hfull0 = mapa_shared(smem_u32(hfull_bar), 0);
       const int brow = static_cast<int>(rank) * (kTcBlockN / 2);
+      uint32_t rphase = 0;
       for (int u = u0; ok && u < units; u += ustep) {
         int n, x0, y0;
         tc_tile_origin(args, 2 * u + static_cast<int>(rank), n, x0, y0);
         for (int cb = 0; ok && cb < cin_blocks; ++cb) {
-          if (!mbar_wait(&hempty_bar[hb], hphase ^ 1u, abort_flag, args.status,
-                         kDevTimeoutProducer)) {
-            ok = false;
-            break;
-          }
-          if (leader) mbar_arrive_expect_tx(&hfull_bar[hb], 2 * kHaloRows * 128);
-          tma_load_4d_pair(smem_halo + hb * kHaloBytes, &map_a, hfull0 + hb * 8u,
-                           cb * kKbElems<T>, x0 - 1, y0 - 1, n, kPolicyEvictLast);
-          if (++hb == kHaloBufs) {
-            hb = 0;
-            hphase ^= 1u;
+          if constexpr (kCvt) {
+            // bf16 halo (channels cb*128 .. +127 as two 64-channel boxes) for the converter
+            if (!mbar_wait(rempty_bar, rphase ^ 1u, abort_flag, args.status,
+                           kDevTimeoutProducer)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(rfull_bar, 2 * kHaloRows * 128);
+            for (int j = 0; j < 2; ++j)
+              tma_load_4d(smem_rawbuf + j * kHaloBytes, &map_a, rfull_bar, cb * 128 + j * 64,
+                          x0 - 1, y0 - 1, n, kPolicyEvictLast);
+            rphase ^= 1u;
+          } else {
+            if (!mbar_wait(&hempty_bar[hb], hphase ^ 1u, abort_flag, args.status,
+                           kDevTimeoutProducer)) {
+              ok = false;
+              break;
+            }
+            if (leader) mbar_arrive_expect_tx(&hfull_bar[hb], 2 * kHaloRows * 128);
+            tma_load_4d_pair(smem_halo + hb * kHaloBytes, &map_a, hfull0 + hb * 8u,
+                             cb * kKbElems<T>, x0 - 1, y0 - 1, n, kPolicyEvictLast);
+            if (++hb == kHaloBufs) {
+              hb = 0;
+              hphase ^= 1u;
+            }
           }
           for (int tap = 0; tap < 9; ++tap) {
             if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, args.status,
@@ -216,10 +251,65 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc_commit_pair_local(done_bar);
       mbar_wait_drain(done_bar, 0);
     }
-  } else {
+  } else if (warp < 2 + kTcEpiWarps) {
     tc_epilogue<1, T, true>(args, &map_out, tmem_base, accf_bar, acce_bar, smem_stage,
                             abort_flag, warp, lane, false,
                             mapa_shared(smem_u32(acce_bar), 0));
+  } else if constexpr (kCvt) {
+    // ------------------------------------------------------------ converter (each CTA)
+    const int ct = threadIdx.x - 32 * (2 + kTcEpiWarps);  // 0 .. 32 * kPairCvtWarps - 1
+    const uint32_t hfull0 = mapa_shared(smem_u32(hfull_bar), 0);
+    const uint32_t raw_addr0 = smem_u32(smem_rawbuf);
+    int hb = 0;
+    uint32_t hphase = 0, rphase = 0;
+    bool ok = true;
+    for (int u = u0; ok && u < units; u += ustep) {
+      const int tile = 2 * u + static_cast<int>(rank);
+      int n, x0, y0;
+      tc_tile_origin(args, tile, n, x0, y0);
+      // virtual tile (past the end): its halo is all padding, any finite scale will do
+      const unsigned am = tile < args.num_tiles ? __ldg(args.in_amax + n) : 0u;
+      const float inv = e4m3_inv_of(am);
+      for (int cb = 0; ok && cb < cin_blocks; ++cb) {
+        bool w = mbar_wait(rfull_bar, rphase, abort_flag, args.status, kDevTimeoutProducer);
+        if (w) w = mbar_wait(&hempty_bar[hb], hphase ^ 1u, abort_flag, args.status,
+                             kDevTimeoutProducer);
+        if (!__all_sync(0xffffffffu, w)) {
+          ok = false;
+          break;
+        }
+        const uint32_t dst0 = smem_u32(smem_halo + hb * kHaloBytes);
+        // item = (halo row r, 16-channel group g): 32 bf16 bytes -> 16 e4m3 bytes
+        for (int it = ct; it < kHaloRows * 8; it += 32 * kPairCvtWarps) {
+          const int r = it >> 3, g = it & 7;
+          const uint32_t src = raw_addr0 + (g >> 2) * kHaloBytes + r * 128;
+          const int c0 = (g & 3) * 2;
+          const uint4 lo = ld_shared_v4(src + (((c0) ^ (r & 7)) << 4));
+          const uint4 hi = ld_shared_v4(src + (((c0 + 1) ^ (r & 7)) << 4));
+          const float2 f0 = Pack<__nv_bfloat16>::unpack(lo.x), f1 = Pack<__nv_bfloat16>::unpack(lo.y);
+          const float2 f2 = Pack<__nv_bfloat16>::unpack(lo.z), f3 = Pack<__nv_bfloat16>::unpack(lo.w);
+          const float2 f4 = Pack<__nv_bfloat16>::unpack(hi.x), f5 = Pack<__nv_bfloat16>::unpack(hi.y);
+          const float2 f6 = Pack<__nv_bfloat16>::unpack(hi.z), f7 = Pack<__nv_bfloat16>::unpack(hi.w);
+          uint4 q;
+          q.x = tc_e4m3x4(f0.x, f0.y, f1.x, f1.y, inv);
+          q.y = tc_e4m3x4(f2.x, f2.y, f3.x, f3.y, inv);
+          q.z = tc_e4m3x4(f4.x, f4.y, f5.x, f5.y, inv);
+          q.w = tc_e4m3x4(f6.x, f6.y, f7.x, f7.y, inv);
+          st_shared_v4(dst0 + r * 128 + ((g ^ (r & 7)) << 4), q);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(rempty_bar);                       // raw buffer consumed
+          mbar_arrive_cluster(hfull0 + hb * 8u);         // e4m3 halo ready (leader's barrier)
+        }
+        rphase ^= 1u;
+        if (++hb == kHaloBufs) {
+          hb = 0;
+          hphase ^= 1u;
+        }
+      }
+    }
   }
 
   tc_fence_before();

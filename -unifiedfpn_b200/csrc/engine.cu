@@ -62,9 +62,9 @@ DType to_dtype(FPNDataType t) {
   }
 }
 
-// 3x3 tiling from its tuning code: -1 = halo tiles on CTA pairs (the default), 0 = halo
-// reuse with 8 x 16 tiles on single CTAs, 8..128 = plain tiles of that width (one shifted
-// box per tap).
+// 3x3 tiling from its tuning code: -1 = halo tiles on CTA pairs (the default for large
+// maps), 0 = halo reuse with 8 x 16 tiles on single CTAs, 8..128 = plain tiles of that width
+// (one shifted box per tap).
 constexpr int kDefaultTilingCode = -1;
 int tiling_code(const Conv3x3Tiling& t) { return t.pair ? -1 : (t.halo ? 0 : t.tile_w); }
 Conv3x3Tiling tiling_from_code(int tw) {
@@ -486,7 +486,15 @@ struct UnifiedFPNCore::Impl {
         check(cudaStreamWaitEvent(side, ev_lat[l], 0), "event");
       }
       const long long n = static_cast<long long>(batch) * H[l] * W[l] * cout;
-      if (quantise)
+      Conv3x3Tiling t = tiling_for(l);
+      if (!t.halo) t = ufpn::halo_pair_tiling();  // e4m3 runs halo tiles only
+      // The CTA-pair 3x3 can quantise M_l itself (per image, in shared memory; no quantise
+      // pass, no e4m3 copy of M_l), but its bf16 staging costs two of the eight weight
+      // stages of this weight-feed-bound kernel: measured 240 us against 181 + 43 us for
+      // quantise-then-convolve at the P2 map of the 640x640 batch-16 workload.  Off.
+      constexpr bool kQuantiseInKernel = false;
+      const bool in_kernel = kQuantiseInKernel && t.pair;
+      if (quantise && !in_kernel)
         ok(ufpn::launch_quantize_e4m3(DType::BF16, merged[l], n, batch, fp8_amax + l * batch,
                                       qmerged[l], fp8_scale + l * batch, conv_stream),
            "quantise merged map");
@@ -494,12 +502,11 @@ struct UnifiedFPNCore::Impl {
       sc.ascale = fp8_scale + l * batch;
       sc.ascale_per_image = true;
       sc.wscale = out_ws[l];
+      if (in_kernel) sc.in_amax = fp8_amax + l * batch;
       TcPlan conv;
-      Conv3x3Tiling t = tiling_for(l);
-      if (!t.halo) t = ufpn::halo_pair_tiling();  // e4m3 runs halo tiles only
-      check(ufpn::plan_tc_conv3x3(conv, DType::E4M3, qmerged[l], out_wp[l], out_b[l], out[l],
-                                  l == 3 ? p6 : nullptr, batch, H[l], W[l], t,
-                                  d_status, 0, sc),
+      check(ufpn::plan_tc_conv3x3(conv, DType::E4M3, in_kernel ? merged[l] : qmerged[l],
+                                  out_wp[l], out_b[l], out[l], l == 3 ? p6 : nullptr, batch,
+                                  H[l], W[l], t, d_status, 0, sc),
             "plan e4m3 conv3x3");
       ok(ufpn::launch_tc(conv, conv_stream), "e4m3 conv3x3 launch");
     };
@@ -624,7 +631,10 @@ void UnifiedFPNCore::configure_levels(const std::vector<FPNDimensions>& dims, in
     m.cin[l] = dims[l].channels;
     m.H[l] = dims[l].height;
     m.W[l] = dims[l].width;
-    m.tiling[l] = tiling_from_code(kDefaultTilingCode);
+    // CTA pairs pay off on large maps only (measured: single-CTA halo tiles are faster up
+    // to a few hundred tiles, where the pair's longer fill and tail dominate).
+    const long long tiles = static_cast<long long>(N) * ((m.H[l] + 15) / 16) * ((m.W[l] + 7) / 8);
+    m.tiling[l] = tiling_from_code(tiles >= 4LL * ufpn::sm_count() ? kDefaultTilingCode : 0);
     m.tiling_tuned[l] = false;
     auto it = m.tuning_db.find(m.tuning_key(l));
     if (it != m.tuning_db.end()) {

@@ -654,7 +654,11 @@ cudaError_t upsample_add_t(const void* coarse, const void* lat, void* out, int N
         const long long blocks = static_cast<long long>(N) * H * chunks;
         int grid = blocks < (1LL << 30) ? static_cast<int>(blocks) : (1 << 30);
         int per = 0;
-        if (amax) {  // contiguous runs: 8 resident 256-thread blocks per SM
+        if (amax) {
+          // With an absmax: contiguous runs of units per block (8 resident 256-thread blocks
+          // per SM), so a block crosses few image boundaries and publishes a handful of
+          // block-reduced maxima.  (One unit per block with a block reduction each measured
+          // 1.5x slower: 12800 reductions at the 640x640 batch-16 P3 map.)
           const long long g = blocks < 148LL * 8 ? blocks : 148LL * 8;
           per = static_cast<int>((blocks + g - 1) / g);
           grid = static_cast<int>((blocks + per - 1) / per);

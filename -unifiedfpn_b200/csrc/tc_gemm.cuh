@@ -152,6 +152,9 @@ struct TcGemmArgs {
   // lateral top-down k-block: precomputed Wb table (tc_wb_table_kernel), or null to build
   // Wb per tile in the producer warp
   const uint8_t* wb_table;
+  // e4m3 3x3 that quantises its bf16 input in shared memory: per-image absmax of the input
+  // (fp32 bits); the activation scale is then amax[n] / 448 (ascale unused)
+  const unsigned* in_amax;
 };
 
 template <typename T>
@@ -199,6 +202,17 @@ __device__ __forceinline__ uint32_t tc_e4m3x4(float a, float b, float c, float d
   const uint32_t hi =
       __nv_cvt_float2_to_fp8x2(make_float2(c * inv, d * inv), __NV_SATFINITE, __NV_E4M3);
   return lo | (hi << 16);
+}
+
+// The quantiser's inverse and dequantisation scale from an absmax (fp32 bits):
+// amax > 0: 448 / amax and amax / 448 (single correctly rounded divisions); else 1.
+__device__ __forceinline__ float e4m3_inv_of(unsigned amax_bits) {
+  const float a = __uint_as_float(amax_bits);
+  return a > 0.f ? __fdiv_rn(448.f, a) : 1.f;
+}
+__device__ __forceinline__ float e4m3_scale_of(unsigned amax_bits) {
+  const float a = __uint_as_float(amax_bits);
+  return a > 0.f ? __fdiv_rn(a, 448.f) : 1.f;
 }
 
 __device__ __forceinline__ void tc_tile_origin(const TcGemmArgs& a, int tile, int& n, int& x0,
@@ -389,7 +403,9 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
     const int py = y0 + row / tw;
     const int px = x0 + row % tw;
     const bool valid = real && (py < args.H) && (px < args.W);
-    const float ascale = (kFp8 && real) ? __ldg(args.ascale + n * args.ascale_stride) : 1.f;
+    const float ascale = !(kFp8 && real) ? 1.f
+                         : args.in_amax != nullptr ? e4m3_scale_of(__ldg(args.in_amax + n))
+                                                   : __ldg(args.ascale + n * args.ascale_stride);
     uint32_t amax_bits = 0;  // max |stored value| of this thread in this tile (fp32 bits)
     const int omode = args.out_mode;
     float qinv = 1.f;

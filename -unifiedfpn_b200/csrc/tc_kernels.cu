@@ -168,15 +168,15 @@ cudaError_t launch_halo_t(const TcPlan& p, cudaStream_t s) {
   return cudaGetLastError();
 }
 
-template <typename T>
+template <typename T, bool kCvt = false>
 cudaError_t launch_halo_pair_t(const TcPlan& p, cudaStream_t s) {
   static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(fpn_conv3x3_halo_pair_kernel<T>,
+    cudaError_t e = cudaFuncSetAttribute(fpn_conv3x3_halo_pair_kernel<T, kCvt>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         PairCfg::kSmemBytes);
+                                         PairCfgT<kCvt>::kSmemBytes);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
@@ -184,8 +184,8 @@ cudaError_t launch_halo_pair_t(const TcPlan& p, cudaStream_t s) {
   std::memcpy(&a, p.args, sizeof(a));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(p.grid), 1, 1);
-  cfg.blockDim = dim3(kTcThreads, 1, 1);
-  cfg.dynamicSmemBytes = PairCfg::kSmemBytes;
+  cfg.blockDim = dim3(PairCfgT<kCvt>::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = PairCfgT<kCvt>::kSmemBytes;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -194,8 +194,8 @@ cudaError_t launch_halo_pair_t(const TcPlan& p, cudaStream_t s) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, fpn_conv3x3_halo_pair_kernel<T>, p.map_a, p.map_b, p.map_out,
-                            a);
+  return cudaLaunchKernelEx(&cfg, fpn_conv3x3_halo_pair_kernel<T, kCvt>, p.map_a, p.map_b,
+                            p.map_out, a);
 }
 
 }  // namespace
@@ -310,7 +310,10 @@ cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w
   const DType odt = fp8 ? DType::BF16 : dt;
   if (!valid_tiling(tiling)) return cudaErrorInvalidValue;
   if (N <= 0 || H <= 0 || W <= 0) return cudaErrorInvalidValue;
-  if (fp8 && (!sc.ascale || !sc.wscale || !tiling.halo)) return cudaErrorInvalidValue;
+  // in_amax (e4m3 only): x is the bf16 map, quantised per image inside the kernel
+  const bool cvt = fp8 && sc.in_amax != nullptr;
+  if (fp8 && ((!sc.ascale && !cvt) || !sc.wscale || !tiling.halo)) return cudaErrorInvalidValue;
+  if (cvt && !tiling.pair) return cudaErrorInvalidValue;
   if (!aligned16(out) || (p6 && !aligned16(p6)) || !aligned16(bias) ||
       (fp8 && !aligned16(sc.wscale)))
     return cudaErrorMisalignedAddress;
@@ -332,13 +335,15 @@ cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w
   a.ascale_stride = sc.ascale_per_image ? 1 : 0;
   a.wscale = sc.wscale;
   a.amax_out = sc.amax_out;
+  a.in_amax = sc.in_amax;
   const bool halo = tiling.halo;
   if (halo && (tiling.tile_w != kHaloTileW || tiling.tile_h != kHaloTileH))
     return cudaErrorInvalidValue;
   if (tiling.pair && !halo) return cudaErrorInvalidValue;
-  // Halo path: one (tile_w + 2) x (tile_h + 2) box per channel block, origin (-1, -1).
-  cudaError_t e = halo ? encode_nhwc(&plan.map_a, dt, x, N, H, W, C, kHaloTileW + 2,
-                                     kHaloTileH + 2)
+  // Halo path: one (tile_w + 2) x (tile_h + 2) box per channel block, origin (-1, -1)
+  // (bf16 boxes of 64 channels when the kernel quantises its input itself).
+  cudaError_t e = halo ? encode_nhwc(&plan.map_a, cvt ? DType::BF16 : dt, x, N, H, W, C,
+                                     kHaloTileW + 2, kHaloTileH + 2)
                        : encode_nhwc(&plan.map_a, dt, x, N, H, W, C, tiling.tile_w, tiling.tile_h);
   if (e != cudaSuccess) return e;
   if ((e = encode_weights(&plan.map_b, dt, w, 9 * C, tiling.pair ? kTcBlockN / 2 : kTcBlockN)) !=
@@ -349,7 +354,7 @@ cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w
     return e;
   plan.map_coarse = plan.map_out;
   std::memcpy(plan.args, &a, sizeof(a));
-  plan.mode = tiling.pair ? 3 : (halo ? 2 : 1);
+  plan.mode = cvt ? 4 : (tiling.pair ? 3 : (halo ? 2 : 1));
   plan.dtype = dt;
   plan.num_tiles = a.num_tiles;
   const int cap = max_ctas > 0 ? max_ctas : sm_count();
@@ -571,6 +576,7 @@ cudaError_t launch_tc(const TcPlan& plan, cudaStream_t s) {
     if (plan.mode == 0) return launch_t<0, __nv_fp8_e4m3>(plan, s);
     if (plan.mode == 2) return launch_halo_t<__nv_fp8_e4m3>(plan, s);
     if (plan.mode == 3) return launch_halo_pair_t<__nv_fp8_e4m3>(plan, s);
+    if (plan.mode == 4) return launch_halo_pair_t<__nv_fp8_e4m3, true>(plan, s);
     return cudaErrorInvalidValue;
   }
   if (plan.mode == 3) {

@@ -84,6 +84,9 @@ SIGNATURES = {
     "ufpn_conv3x3_e4m3": (
         c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                 c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "ufpn_conv3x3_e4m3_from_bf16": (
+        c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                c_int, c_int, c_int, c_void_p]),
     "ufpn_core_forward_e4m3": (
         c_int, [c_void_p, POINTER(c_void_p), POINTER(c_void_p), POINTER(c_void_p), c_void_p, c_void_p]),
     "ufpn_neck_forward_noalloc": (

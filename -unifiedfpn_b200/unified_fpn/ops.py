@@ -298,6 +298,29 @@ def fpn_conv3x3_fp8(input: torch.Tensor, input_scale, weight: torch.Tensor,
     return (out, p6t) if p6 else out
 
 
+def fpn_conv3x3_fp8_from_bf16(input: torch.Tensor, amax_bits: torch.Tensor, weight: torch.Tensor,
+                              weight_scales: torch.Tensor, bias: torch.Tensor, p6: bool = False):
+    """FP8 3x3 on CTA pairs that quantises its bf16 ``input`` per image inside the kernel:
+    ``amax_bits`` (int32 [N]) holds each image's absmax as fp32 bits; the result equals
+    ``fpn_conv3x3_fp8(*quantize_fp8(input, per_image=True), ...)`` bit for bit."""
+    _check_cuda(input, amax_bits, weight, weight_scales, bias)
+    x = input.contiguous(memory_format=torch.channels_last)
+    N, C, H, W = x.shape
+    if x.dtype != torch.bfloat16 or C != 256 or weight.dtype != E4M3:
+        raise ValueError("expects a bf16 [N, 256, H, W] input and an e4m3 packed weight")
+    ws = weight_scales.to(torch.float32).contiguous()
+    b = bias.to(device=x.device, dtype=torch.float32).contiguous()
+    out = torch.empty((N, 256, H, W), dtype=torch.bfloat16, device=x.device,
+                      memory_format=torch.channels_last)
+    p6t = torch.empty((N, 256, (H - 1) // 2 + 1, (W - 1) // 2 + 1), dtype=torch.bfloat16,
+                      device=x.device, memory_format=torch.channels_last) if p6 else None
+    check(lib.ufpn_conv3x3_e4m3_from_bf16(x.data_ptr(), amax_bits.contiguous().data_ptr(),
+                                          weight.contiguous().data_ptr(), ws.data_ptr(), b.data_ptr(),
+                                          out.data_ptr(), p6t.data_ptr() if p6t is not None else None,
+                                          N, H, W, _stream(x)), "ufpn_conv3x3_e4m3_from_bf16")
+    return (out, p6t) if p6 else out
+
+
 def device_status(reset: bool = True) -> int:
     """Status word of the standalone tensor-core ops on the current device (0 = ok)."""
     v = _lib.c_int(0)

@@ -110,7 +110,8 @@ struct TcPlan {
   alignas(64) CUtensorMap map_out;
   alignas(64) CUtensorMap map_coarse;
   unsigned char args[256];  // TcGemmArgs, opaque outside tc_kernels.cu
-  int mode = 0;             // 0 lateral, 1 conv3x3, 2 conv3x3 halo, 3 conv3x3 halo on CTA pairs
+  int mode = 0;  // 0 lateral, 1 conv3x3, 2 conv3x3 halo, 3 halo on CTA pairs, 4 the same + e4m3
+                 // quantisation of a bf16 input in shared memory
   DType dtype = DType::BF16;
   int grid = 0;
   int num_tiles = 0;
@@ -136,6 +137,10 @@ struct TcScales {
   int out_mode = 0;
   const unsigned* qamax = nullptr;
   float* qscale_out = nullptr;
+  // E4M3 3x3 on CTA pairs only: x is the bf16 map and in_amax[n] its per-image absmax
+  // (fp32 bits); the kernel quantises each halo itself (e4m3(x * 448 / amax), the same
+  // codes as launch_quantize_e4m3) and scales by amax / 448 (ascale unused).
+  const unsigned* in_amax = nullptr;
 };
 
 // Lateral 1x1 (+ optional fused bilinear upsample-add of the coarser merged map).

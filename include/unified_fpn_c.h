@@ -212,6 +212,12 @@ int ufpn_lateral_conv_e4m3(const void* x, const float* x_scale, int x_scale_per_
 int ufpn_conv3x3_e4m3(const void* x, const float* x_scale, int x_scale_per_image, const void* w,
                       const float* w_scales, const float* bias, void* out, void* p6, int N,
                       int H, int W, int tile_w, unsigned* amax_out, void* stream);
+/* The same FP8 3x3 (CTA pairs) on a bf16 input x [N][H][W][256] with per-image absmax
+ * amax_bits[N] (fp32 bits): each halo is quantised in shared memory to exactly the codes
+ * ufpn_quantize_e4m3 (groups = N) would store, and scaled by amax / 448. */
+int ufpn_conv3x3_e4m3_from_bf16(const void* x, const unsigned* amax_bits, const void* w,
+                                const float* w_scales, const float* bias, void* out, void* p6,
+                                int N, int H, int W, void* stream);
 /* fpn_engine.cu:191-245 (forward) for an engine configured with dtype UFPN_DTYPE_E4M3
  * (NHWC): inputs C2..C5 e4m3, input_scales[l] = device fp32 per-tensor scale of inputs[l];
  * outputs P2..P5 (and p6) bf16.  Each merged map M_l is quantised per image before its 3x3,

@@ -141,6 +141,26 @@ def test_conv3x3_fp8_matches_oracle(cuda_device, shape, per_image):
     assert torch.equal(p6.cpu(), out[:, :, ::2, ::2].cpu())
 
 
+@pytest.mark.parametrize("shape", [(2, 40, 56), (1, 25, 38), (3, 13, 21), (16, 160, 160)])
+def test_conv3x3_fp8_in_kernel_quantisation(cuda_device, shape):
+    """The CTA-pair e4m3 3x3 that quantises its bf16 input per image in shared memory gives
+    bitwise what quantising first (the standalone quantiser) and convolving gives."""
+    import unified_fpn as U
+    N, H, W = shape
+    g = torch.Generator(device="cuda").manual_seed(15)
+    m = _cl(torch.randn(N, 256, H, W, device="cuda", generator=g).to(torch.bfloat16))
+    w3 = torch.randn(256, 256, 3, 3, device="cuda", generator=g) * (2.0 / 2304) ** 0.5
+    b = (torch.rand(256, device="cuda", generator=g) * 2 - 1) * 0.1
+    qw, sw = U.quantize_fp8_rows(w3, pack3x3=True)
+    qm, sm = U.quantize_fp8(m, per_image=True)
+    ref, ref6 = U.fpn_conv3x3_fp8(qm, sm, qw, sw, b, p6=True, tile_w=-1)
+    amax = m.float().abs().amax(dim=(1, 2, 3)).contiguous().view(torch.int32)
+    out, p6 = U.fpn_conv3x3_fp8_from_bf16(m, amax, qw, sw, b, p6=True)
+    torch.cuda.synchronize()
+    assert U.device_status() == 0
+    assert torch.equal(out, ref) and torch.equal(p6, ref6)
+
+
 def _fp8_case(batch, chans, sizes, seed, bias_scale=0.1):
     feats = O.make_features(batch, chans, sizes, seed=seed, dist="normal")
     wts = O.make_weights(chans, seed=seed + 1, bias_scale=bias_scale)
