@@ -125,6 +125,7 @@ struct UnifiedFPNCore::Impl {
   cudaEvent_t ev_fork = nullptr;
   cudaEvent_t ev_lat[4] = {};
   cudaEvent_t ev_join = nullptr;
+  cudaEvent_t ev_join_lat[2] = {};  // joins of the P4 / P3 3x3 streams
   cudaEvent_t prof[10] = {};
   FPNKernelConfig cfg;
   Conv3x3Tiling tiling[4];
@@ -205,6 +206,8 @@ struct UnifiedFPNCore::Impl {
     }
     if (ev_fork) cudaEventDestroy(ev_fork);
     if (ev_join) cudaEventDestroy(ev_join);
+    for (auto& e : ev_join_lat)
+      if (e) cudaEventDestroy(e);
     for (auto& e : ev_lat)
       if (e) cudaEventDestroy(e);
     for (auto& e : prof)
@@ -358,18 +361,15 @@ struct UnifiedFPNCore::Impl {
       return launches;
     }
     const bool one_stream = prof_events || cfg.single_stream;
-    cudaStream_t conv_stream = one_stream ? main : side;
-    if (!one_stream) {
-      check(cudaEventRecord(ev_fork, main), "event");
-      check(cudaStreamWaitEvent(side, ev_fork, 0), "event");
-    }
     // Main stream (the top-down data dependence):
     //   1. ONE grouped launch of the raw P5, P4, P3 laterals L5, L4, L3 (as GEMMs they do
     //      not depend on one another; only their top-down adds chain);
     //   2. in-place merges M4 = L4 + up(M5), M3 = L3 + up(M4) (bandwidth kernels on the
     //      small maps; M5 = L5);
     //   3. the P2 lateral with the top-down add of M3 fused into its epilogue.
-    // Side stream: each level's 3x3 as soon as its merged map exists.
+    // Side streams, one per level: the P5, P4 and P3 3x3s, each as soon as its merged map
+    // exists, so the small P5 / P4 grids run beside the chain instead of one after the
+    // other; the P2 3x3 follows the P2 lateral on the main stream.
     ufpn::NeckLevel lv[4];
     for (int l = 0; l < 4; ++l) {
       lv[l].x = x[l];
@@ -386,20 +386,22 @@ struct UnifiedFPNCore::Impl {
       lv[l].conv_tiling = tiling_for(l);
     }
     auto conv_level = [&](int l) {
-      if (!one_stream) {
+      const cudaStream_t st = conv_stream(l, main, one_stream);
+      if (st != main) {
         check(cudaEventRecord(ev_lat[l], main), "event");
-        check(cudaStreamWaitEvent(side, ev_lat[l], 0), "event");
+        check(cudaStreamWaitEvent(st, ev_lat[l], 0), "event");
       }
       TcPlan conv;
       check(ufpn::plan_tc_conv3x3(conv, dtype, merged[l], out_wp[l], out_b[l], o[l],
                                   l == 3 ? o6 : nullptr, batch, H[l], W[l], tiling_for(l),
                                   d_status, 0),
             "plan conv3x3");
-      ok(ufpn::launch_tc(conv, conv_stream), "conv3x3 launch");
+      ok(ufpn::launch_tc(conv, st), "conv3x3 launch");
     };
     const ufpn::NeckJobSpec grouped[3] = {{0, 3, 0}, {0, 2, 0}, {0, 1, 0}};
     ufpn::NeckPlan gplan;
-    check(ufpn::plan_neck_jobs(gplan, dtype, batch, lv, nullptr, grouped, 3, d_sched, d_status, 0),
+    check(ufpn::plan_neck_jobs(gplan, dtype, batch, lv, nullptr, grouped, 3, d_sched, d_status, 0,
+                               trace_next ? d_trace : nullptr),
           "plan grouped laterals");
     ok(ufpn::launch_neck(gplan, main), "grouped laterals launch");
     if (prof_events) cudaEventRecord(prof[1], main);
@@ -423,30 +425,43 @@ struct UnifiedFPNCore::Impl {
     if (prof_events) cudaEventRecord(prof[7], main);
     conv_level(0);
     if (prof_events) cudaEventRecord(prof[8], main);
+    if (!one_stream) join_conv_streams(main);
     if (nchw) {
       for (int l = 0; l < 4; ++l)
-        ok(ufpn::launch_transpose(dtype, o[l], out[l], batch, cout, H[l] * W[l], false,
-                                  conv_stream),
+        ok(ufpn::launch_transpose(dtype, o[l], out[l], batch, cout, H[l] * W[l], false, main),
            "NHWC->NCHW");
       if (p6)
         ok(ufpn::launch_transpose(dtype, o6, p6, batch, cout,
-                                  ((H[3] - 1) / 2 + 1) * ((W[3] - 1) / 2 + 1), false, conv_stream),
+                                  ((H[3] - 1) / 2 + 1) * ((W[3] - 1) / 2 + 1), false, main),
            "NHWC->NCHW");
     }
-    if (!one_stream) {
-      check(cudaEventRecord(ev_join, side), "event");
-      check(cudaStreamWaitEvent(main, ev_join, 0), "event");
-    }
     return launches;
+  }
+
+  // Stream of level l's 3x3 in the split schedules: P5 on `side`, P4 / P3 on the two
+  // lat_side streams (each after that stream's earlier work, if any), P2 on main.
+  cudaStream_t conv_stream(int l, cudaStream_t main, bool one_stream) const {
+    if (one_stream || l == 0) return main;
+    return l == 3 ? side : lat_side[2 - l];
+  }
+  void join_conv_streams(cudaStream_t main) {
+    check(cudaEventRecord(ev_join, side), "event");
+    check(cudaStreamWaitEvent(main, ev_join, 0), "event");
+    for (int i = 0; i < 2; ++i) {
+      check(cudaEventRecord(ev_join_lat[i], lat_side[i]), "event");
+      check(cudaStreamWaitEvent(main, ev_join_lat[i], 0), "event");
+    }
   }
 
   // e4m3 inputs (NHWC), bf16 M_l and outputs.  Same dependence structure as the 16-bit
   // split schedule; each M_l additionally gets its per-image absmax from the kernel that
   // writes it (P5 / P2 lateral epilogue, P4 / P3 merge) and is quantised to e4m3 per image
-  // on the side stream right before its 3x3 (per image, so an image's result does not
+  // on its 3x3's stream right before the 3x3 (per image, so an image's result does not
   // depend on the rest of its batch, e.g. on how a batch is sharded over GPUs):
-  //   main:  zero amax | lat5 (amax5) lat4 lat3 | merge4 (amax4) | merge3 (amax3, M3s) | lat2 + up(M3s) (amax2)
-  //   side:              q5 3x3_5 (+P6)        q4 3x3_4         q3 3x3_3          q2 3x3_2
+  //   main:        zero amax | lat5 (amax5) | merge4 (amax4) | merge3 (amax3, M3s) | lat2 + up(M3s) (amax2) | q2 3x3_2
+  //   side:                                  q5 3x3_5 (+P6)
+  //   lat_side[0]:             lat4                            q4 3x3_4
+  //   lat_side[1]:             lat3                                                 q3 3x3_3
   int enqueue_e4m3(const void* const* in, void* const* out, void* p6, cudaStream_t main,
                    bool prof_events) {
     int launches = 0;
@@ -455,13 +470,11 @@ struct UnifiedFPNCore::Impl {
       ++launches;
     };
     const bool one_stream = prof_events || cfg.single_stream;
-    const cudaStream_t conv_stream = one_stream ? main : side;
     if (prof_events) cudaEventRecord(prof[0], main);
     check(cudaMemsetAsync(fp8_amax, 0, 4 * static_cast<size_t>(batch) * sizeof(unsigned), main),
           "memset");
     if (!one_stream) {
       check(cudaEventRecord(ev_fork, main), "event");
-      check(cudaStreamWaitEvent(side, ev_fork, 0), "event");
       for (int i = 0; i < 2; ++i) check(cudaStreamWaitEvent(lat_side[i], ev_fork, 0), "event");
     }
     auto lateral = [&](int l, const void* coarse, unsigned* amax_out, cudaStream_t st) {
@@ -481,9 +494,10 @@ struct UnifiedFPNCore::Impl {
     };
     // quantise = false: qmerged[l] and its scales were written by the kernel producing M_l.
     auto conv_level = [&](int l, bool quantise = true) {
-      if (!one_stream) {
+      const cudaStream_t conv_st = conv_stream(l, main, one_stream);
+      if (conv_st != main) {
         check(cudaEventRecord(ev_lat[l], main), "event");
-        check(cudaStreamWaitEvent(side, ev_lat[l], 0), "event");
+        check(cudaStreamWaitEvent(conv_st, ev_lat[l], 0), "event");
       }
       const long long n = static_cast<long long>(batch) * H[l] * W[l] * cout;
       Conv3x3Tiling t = tiling_for(l);
@@ -496,7 +510,7 @@ struct UnifiedFPNCore::Impl {
       const bool in_kernel = kQuantiseInKernel && t.pair;
       if (quantise && !in_kernel)
         ok(ufpn::launch_quantize_e4m3(DType::BF16, merged[l], n, batch, fp8_amax + l * batch,
-                                      qmerged[l], fp8_scale + l * batch, conv_stream),
+                                      qmerged[l], fp8_scale + l * batch, conv_st),
            "quantise merged map");
       ufpn::TcScales sc;
       sc.ascale = fp8_scale + l * batch;
@@ -508,7 +522,7 @@ struct UnifiedFPNCore::Impl {
                                   out_wp[l], out_b[l], out[l], l == 3 ? p6 : nullptr, batch,
                                   H[l], W[l], t, d_status, 0, sc),
             "plan e4m3 conv3x3");
-      ok(ufpn::launch_tc(conv, conv_stream), "e4m3 conv3x3 launch");
+      ok(ufpn::launch_tc(conv, conv_st), "e4m3 conv3x3 launch");
     };
     // The three raw laterals are independent GEMMs: P5 on the main stream, P4 and P3 on
     // their own streams so the small P5 grid shares the machine with the larger ones.
@@ -541,10 +555,7 @@ struct UnifiedFPNCore::Impl {
     if (prof_events) cudaEventRecord(prof[7], main);
     conv_level(0);
     if (prof_events) cudaEventRecord(prof[8], main);
-    if (!one_stream) {
-      check(cudaEventRecord(ev_join, side), "event");
-      check(cudaStreamWaitEvent(main, ev_join, 0), "event");
-    }
+    if (!one_stream) join_conv_streams(main);
     return launches;
   }
 
@@ -583,6 +594,7 @@ UnifiedFPNCore::UnifiedFPNCore(size_t workspace_size, int device) : impl_(new Im
   }
   CUDA_CHECK(cudaEventCreateWithFlags(&impl_->ev_fork, cudaEventDisableTiming));
   CUDA_CHECK(cudaEventCreateWithFlags(&impl_->ev_join, cudaEventDisableTiming));
+  for (auto& e : impl_->ev_join_lat) CUDA_CHECK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   for (auto& e : impl_->ev_lat) CUDA_CHECK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   for (auto& e : impl_->prof) CUDA_CHECK(cudaEventCreate(&e));
   CUDA_CHECK(cudaMalloc(&impl_->d_status, 1024));

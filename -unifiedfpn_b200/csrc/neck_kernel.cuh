@@ -225,12 +225,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       int issued = 0;
       bool ok = true;
       int ready_level_mask = 0;  // dependency levels already observed complete
-      // The next tile number is fetched one tile ahead so the atomic's round trip
-      // overlaps the current tile's loads instead of stalling between tiles.
+      // The next tile number is claimed while the current tile's last k-block is issued:
+      // the atomic's round trip overlaps the MMAs still queued for this tile, and a CTA
+      // held by a long tile (a P5 lateral has 32 k-blocks) does not sit on a second tile
+      // that an idle CTA could have taken (claimed one whole tile ahead, such a tile
+      // started only when the long one ended and set the end of the launch).
       int t_next = atomicAdd(&sched[0], 1);
       while (ok) {
         const int t = t_next;
-        if (t < P.total_tiles) t_next = atomicAdd(&sched[0], 1);
+        t_next = P.total_tiles;
         if (!mbar_wait(&rempty_bar[rslot], rphase ^ 1u, abort_flag, P.status,
                        kDevTimeoutProducer)) {
           ok = false;
@@ -274,6 +277,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                       x0 + dx, y0 + dy, n, jb.mode == 0 ? kPolicyEvictFirst : kPolicyEvictLast);
           tma_load_2d(smem_b + stage * kTcBStage, &jb.map_b, &full_bar[stage], kb * kTcBlockK, 0,
                       kPolicyEvictLast);
+          if (kb == jb.num_kb - 1) t_next = atomicAdd(&sched[0], 1);
           ++issued;
           if (++stage == S) {
             stage = 0;
@@ -573,6 +577,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       } else if (staged) {
         epi_bar_sync();  // every warp is done reading this tile's coarse box
       }
+      if (P.trace && lateral && !jb.publish && leader)
+        atomicMax(&P.trace[1 + jb.level], globaltimer_ns());  // stores issued, not complete
       // The coarse buffer is free (lateral tiles passed the barrier above; other
       // tiles do not read it): prefetch the next tile's coarse box if that tile is
       // a lateral with a top-down add.
