@@ -224,6 +224,16 @@ int ufpn_core_set_schedule(ufpn_core* core, int fused_neck_kernel) {
   });
 }
 
+int ufpn_core_set_programmatic_launch(ufpn_core* core, int enable) {
+  if (!core) return fail(UFPN_ERR_INVALID_ARG, "NULL core");
+  return guarded([&] {
+    FPNKernelConfig c = core->core.get_kernel_config();
+    c.programmatic_launch = enable != 0;
+    core->core.set_kernel_config(c);
+    return UFPN_OK;
+  });
+}
+
 size_t ufpn_core_get_memory_usage(const ufpn_core* core) {
   return core ? core->core.get_memory_usage() : 0;
 }

@@ -131,6 +131,7 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
   cluster_sync_all();  // barriers initialised and TMEM allocated in BOTH CTAs
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();  // (programmatic launch) the previous kernel's results are visible
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer (each CTA)
@@ -188,6 +189,7 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
           }
         }
       }
+      griddep_launch_dependents();  // this CTA's last loads are issued
       // Copies in flight complete on the leader's barriers; after an abort, give them time
       // to land before this CTA's shared memory can go away.
       if (!ok) pair_settle_ns(1000000);

@@ -361,6 +361,9 @@ struct UnifiedFPNCore::Impl {
       return launches;
     }
     const bool one_stream = prof_events || cfg.single_stream;
+    // Programmatic dependent launches for every kernel that follows a kernel of ours on its
+    // stream (not under profiling events, which time kernels one by one).
+    const bool pdl = !prof_events && cfg.programmatic_launch;
     // Main stream (the top-down data dependence):
     //   1. ONE grouped launch of the raw P5, P4, P3 laterals L5, L4, L3 (as GEMMs they do
     //      not depend on one another; only their top-down adds chain);
@@ -396,7 +399,9 @@ struct UnifiedFPNCore::Impl {
                                   l == 3 ? o6 : nullptr, batch, H[l], W[l], tiling_for(l),
                                   d_status, 0),
             "plan conv3x3");
-      ok(ufpn::launch_tc(conv, st), "conv3x3 launch");
+      // (on the main stream the 3x3 follows a kernel: the P2 lateral, or the previous
+      // level's merge / 3x3 when every kernel runs on one stream)
+      ok(ufpn::launch_tc(conv, st, pdl && st == main), "conv3x3 launch");
     };
     const ufpn::NeckJobSpec grouped[3] = {{0, 3, 0}, {0, 2, 0}, {0, 1, 0}};
     ufpn::NeckPlan gplan;
@@ -409,7 +414,8 @@ struct UnifiedFPNCore::Impl {
     if (prof_events) cudaEventRecord(prof[2], main);
     for (int l = 2; l >= 1; --l) {
       ok(ufpn::launch_upsample_add(dtype, merged[l + 1], merged[l], merged[l], batch, cout,
-                                   H[l + 1], W[l + 1], H[l], W[l], 0, Layout::NHWC, main),
+                                   H[l + 1], W[l + 1], H[l], W[l], 0, Layout::NHWC, main, nullptr,
+                                   nullptr, pdl),
          "merge");
       if (prof_events) cudaEventRecord(prof[3 + 2 * (2 - l)], main);
       conv_level(l);
@@ -421,7 +427,7 @@ struct UnifiedFPNCore::Impl {
                                 0),
           "plan lateral");
     ufpn::tc_attach_wb_table(lat2, wb_table);
-    ok(ufpn::launch_tc(lat2, main), "lateral launch");
+    ok(ufpn::launch_tc(lat2, main, pdl), "lateral launch");
     if (prof_events) cudaEventRecord(prof[7], main);
     conv_level(0);
     if (prof_events) cudaEventRecord(prof[8], main);
@@ -470,6 +476,10 @@ struct UnifiedFPNCore::Impl {
       ++launches;
     };
     const bool one_stream = prof_events || cfg.single_stream;
+    // Programmatic dependent launches measured 2-5% slower on this schedule at the 640x640
+    // batch-16 workload (its quantisation kernels release their dependents at their start,
+    // so the next 3x3's CTAs wait on SMs the other streams could use): off.
+    const bool pdl = false;
     if (prof_events) cudaEventRecord(prof[0], main);
     check(cudaMemsetAsync(fp8_amax, 0, 4 * static_cast<size_t>(batch) * sizeof(unsigned), main),
           "memset");
@@ -477,7 +487,8 @@ struct UnifiedFPNCore::Impl {
       check(cudaEventRecord(ev_fork, main), "event");
       for (int i = 0; i < 2; ++i) check(cudaStreamWaitEvent(lat_side[i], ev_fork, 0), "event");
     }
-    auto lateral = [&](int l, const void* coarse, unsigned* amax_out, cudaStream_t st) {
+    auto lateral = [&](int l, const void* coarse, unsigned* amax_out, cudaStream_t st,
+                       bool after_kernel) {
       ufpn::TcScales sc;
       sc.ascale = in_scale[l];
       sc.wscale = lat_ws[l];
@@ -490,7 +501,7 @@ struct UnifiedFPNCore::Impl {
                                   d_status, 0, sc),
             "plan e4m3 lateral");
       if (l == 0) ufpn::tc_attach_wb_table(p, wb_table);
-      ok(ufpn::launch_tc(p, st), "e4m3 lateral launch");
+      ok(ufpn::launch_tc(p, st, pdl && after_kernel), "e4m3 lateral launch");
     };
     // quantise = false: qmerged[l] and its scales were written by the kernel producing M_l.
     auto conv_level = [&](int l, bool quantise = true) {
@@ -508,9 +519,12 @@ struct UnifiedFPNCore::Impl {
       // quantise-then-convolve at the P2 map of the 640x640 batch-16 workload.  Off.
       constexpr bool kQuantiseInKernel = false;
       const bool in_kernel = kQuantiseInKernel && t.pair;
+      // (on the main stream the quantisation follows the P2 lateral kernel; on a side stream
+      // it follows an event wait)
       if (quantise && !in_kernel)
         ok(ufpn::launch_quantize_e4m3(DType::BF16, merged[l], n, batch, fp8_amax + l * batch,
-                                      qmerged[l], fp8_scale + l * batch, conv_st),
+                                      qmerged[l], fp8_scale + l * batch, conv_st,
+                                      pdl && conv_st == main),
            "quantise merged map");
       ufpn::TcScales sc;
       sc.ascale = fp8_scale + l * batch;
@@ -522,14 +536,15 @@ struct UnifiedFPNCore::Impl {
                                   out_wp[l], out_b[l], out[l], l == 3 ? p6 : nullptr, batch,
                                   H[l], W[l], t, d_status, 0, sc),
             "plan e4m3 conv3x3");
-      ok(ufpn::launch_tc(conv, conv_st), "e4m3 conv3x3 launch");
+      ok(ufpn::launch_tc(conv, conv_st, pdl && (conv_st == main || (quantise && !in_kernel))),
+         "e4m3 conv3x3 launch");
     };
     // The three raw laterals are independent GEMMs: P5 on the main stream, P4 and P3 on
     // their own streams so the small P5 grid shares the machine with the larger ones.
-    lateral(3, nullptr, fp8_amax + 3 * batch, main);
+    lateral(3, nullptr, fp8_amax + 3 * batch, main, false);  // after the memset
     for (int i = 0; i < 2; ++i) {
       const cudaStream_t st = one_stream ? main : lat_side[i];
-      lateral(2 - i, nullptr, nullptr, st);
+      lateral(2 - i, nullptr, nullptr, st, one_stream);
       if (!one_stream) check(cudaEventRecord(ev_lat_done[i], st), "event");
     }
     if (prof_events) cudaEventRecord(prof[1], main);
@@ -545,13 +560,13 @@ struct UnifiedFPNCore::Impl {
       m3s.scale_w = lat_ws[0];
       ok(ufpn::launch_upsample_add(DType::BF16, merged[l + 1], merged[l], merged[l], batch, cout,
                                    H[l + 1], W[l + 1], H[l], W[l], 0, Layout::NHWC, main,
-                                   fp8_amax + l * batch, l == 1 ? &m3s : nullptr),
+                                   fp8_amax + l * batch, l == 1 ? &m3s : nullptr, pdl),
          "merge");
       if (prof_events) cudaEventRecord(prof[3 + 2 * (2 - l)], main);
       conv_level(l);
       if (prof_events) cudaEventRecord(prof[4 + 2 * (2 - l)], main);
     }
-    lateral(0, m3_scaled, fp8_amax, main);
+    lateral(0, m3_scaled, fp8_amax, main, true);
     if (prof_events) cudaEventRecord(prof[7], main);
     conv_level(0);
     if (prof_events) cudaEventRecord(prof[8], main);

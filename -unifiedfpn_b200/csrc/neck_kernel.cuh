@@ -214,6 +214,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();  // (programmatic launch) the previous kernel's results are visible
 
   if (warp == 0) {
     // ------------------------------------------------------------ fetcher + TMA producer
@@ -285,6 +286,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
         }
       }
+      griddep_launch_dependents();  // no tile left for this CTA
       if (!ok) {
         // Unblock the consumers: publish an end marker if a ring slot is free.
         if (mbar_test(smem_u32(&rempty_bar[rslot]), rphase ^ 1u)) {

@@ -43,6 +43,20 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+// Programmatic dependent launch.  A kernel launched with programmatic stream serialisation
+// may be scheduled while the kernel before it in its stream still runs: it sets up (barriers,
+// TMEM, tensor-map prefetch) and then calls griddep_wait(), which returns once that kernel
+// has completed and its memory operations are visible, before it reads or writes any buffer
+// the earlier kernel touches.  griddep_launch_dependents() lets the next kernel be scheduled
+// once every CTA of this grid has called it (or exited).  Without a programmatic dependency
+// both are no-ops.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ uint32_t elect_one_sync() {
   uint32_t pred = 0;
   asm volatile(

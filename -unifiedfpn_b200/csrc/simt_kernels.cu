@@ -8,6 +8,7 @@
 // align_corners), clamped to [0, in-1], y1 = min(y0+1, in-1), weights
 // (1-wy)(1-wx), (1-wy)wx, wy(1-wx), wy*wx.
 #include "kernels.h"
+#include "ptx.cuh"
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -122,6 +123,8 @@ template <typename T, bool kVec>
 __global__ void __launch_bounds__(256) upsample_add_nhwc_kernel(
     const T* __restrict__ coarse, const T* lat, T* out, int N, int C, int Hc, int Wc, int H,
     int W, float sy_scale, float sx_scale, int ac) {
+  griddep_wait();  // (programmatic launch) inputs written by the previous kernel
+  griddep_launch_dependents();
   constexpr int V = kVec ? Vec16<T>::kN : 1;
   const int cvs = C / V;  // channel vectors per pixel
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -209,6 +212,8 @@ __global__ void __launch_bounds__(256) upsample_add_px512_kernel(
     int chunks, float sy_scale, float sx_scale, int ac, unsigned* amax, T* out_s,
     const float* scale_a, const float* scale_w, int units_per_block) {
   static_assert(sizeof(T) == 2, "16-bit types");
+  griddep_wait();  // (programmatic launch) inputs written by the previous kernel
+  griddep_launch_dependents();
   __shared__ unsigned red[8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float inv[8];
@@ -281,6 +286,8 @@ template <typename T>
 __global__ void __launch_bounds__(256) upsample_add_nchw_kernel(
     const T* __restrict__ coarse, const T* __restrict__ lat, T* __restrict__ out, int N, int C,
     int Hc, int Wc, int H, int W, float sy_scale, float sx_scale, int ac) {
+  griddep_wait();  // (programmatic launch) inputs written by the previous kernel
+  griddep_launch_dependents();
   const long long total = static_cast<long long>(N) * C * H * W;
   for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -439,6 +446,8 @@ __device__ __forceinline__ uint32_t e4m3x4(float a, float b, float c, float d, f
 template <typename T>
 __global__ void __launch_bounds__(256) absmax_kernel(const T* __restrict__ x, long long per,
                                                      int vec, unsigned* amax) {
+  griddep_wait();  // (programmatic launch) inputs written by the previous kernel
+  griddep_launch_dependents();
   constexpr int V = Vec16<T>::kN;
   const T* xg = x + static_cast<long long>(blockIdx.y) * per;
   unsigned m = 0;
@@ -462,6 +471,8 @@ __global__ void __launch_bounds__(256) quantize_e4m3_kernel(const T* __restrict_
                                                             int vec, const unsigned* amax,
                                                             uint8_t* __restrict__ q,
                                                             float* scale_out) {
+  griddep_wait();  // (programmatic launch) inputs written by the previous kernel
+  griddep_launch_dependents();
   const unsigned a = amax[blockIdx.y];
   const float inv = e4m3_inv(a);
   if (scale_out && blockIdx.x == 0 && threadIdx.x == 0) scale_out[blockIdx.y] = e4m3_scale(a);
@@ -636,7 +647,7 @@ cudaError_t absmax_t(const void* x, long long n, int groups, unsigned* amax, cud
 template <typename T>
 cudaError_t upsample_add_t(const void* coarse, const void* lat, void* out, int N, int C, int Hc,
                            int Wc, int H, int W, int ac, Layout layout, cudaStream_t s,
-                           unsigned* amax, const MergeScaledCopy* sc) {
+                           unsigned* amax, const MergeScaledCopy* sc, bool pdl) {
   const float sy = (ac && H > 1) ? static_cast<float>(Hc - 1) / (H - 1)
                                  : static_cast<float>(Hc) / H;
   const float sx = (ac && W > 1) ? static_cast<float>(Wc - 1) / (W - 1)
@@ -663,28 +674,30 @@ cudaError_t upsample_add_t(const void* coarse, const void* lat, void* out, int N
           per = static_cast<int>((blocks + g - 1) / g);
           grid = static_cast<int>((blocks + per - 1) / per);
         }
-        upsample_add_px512_kernel<T>
-            <<<grid, 256, 0, s>>>(c, l, o, N, Hc, Wc, H, W, chunks, sy, sx, ac, amax,
-                                  sc ? static_cast<T*>(sc->out) : nullptr,
-                                  sc ? sc->scale_a : nullptr, sc ? sc->scale_w : nullptr, per);
-        return cudaGetLastError();
+        return launch_ex(upsample_add_px512_kernel<T>, dim3(grid), dim3(256), 0, s, pdl, 1, c, l,
+                         o, N, Hc, Wc, H, W, chunks, sy, sx, ac, amax,
+                         sc ? static_cast<T*>(sc->out) : nullptr, sc ? sc->scale_a : nullptr,
+                         sc ? sc->scale_w : nullptr, per);
       }
     }
     if (sc) return cudaErrorNotSupported;  // the scaled copy exists on the 256-channel path
     const long long units =
         static_cast<long long>(N) * H * ((W + 8 * kUpPix - 1) / (8 * kUpPix));  // per block
     const int grid = units < 148 * 64 ? static_cast<int>(units) : 148 * 64;
+    cudaError_t e0;
     if (vec)
-      upsample_add_nhwc_kernel<T, true>
-          <<<grid, 256, 0, s>>>(c, l, o, N, C, Hc, Wc, H, W, sy, sx, ac);
+      e0 = launch_ex(upsample_add_nhwc_kernel<T, true>, dim3(grid), dim3(256), 0, s, pdl, 1, c, l,
+                     o, N, C, Hc, Wc, H, W, sy, sx, ac);
     else
-      upsample_add_nhwc_kernel<T, false>
-          <<<grid, 256, 0, s>>>(c, l, o, N, C, Hc, Wc, H, W, sy, sx, ac);
+      e0 = launch_ex(upsample_add_nhwc_kernel<T, false>, dim3(grid), dim3(256), 0, s, pdl, 1, c,
+                     l, o, N, C, Hc, Wc, H, W, sy, sx, ac);
+    if (e0 != cudaSuccess) return e0;
   } else {
     const long long work = static_cast<long long>(N) * C * H * W;
     if (sc) return cudaErrorNotSupported;
-    upsample_add_nchw_kernel<T>
-        <<<grid_for(work, 256), 256, 0, s>>>(c, l, o, N, C, Hc, Wc, H, W, sy, sx, ac);
+    cudaError_t e0 = launch_ex(upsample_add_nchw_kernel<T>, dim3(grid_for(work, 256)), dim3(256),
+                               0, s, pdl, 1, c, l, o, N, C, Hc, Wc, H, W, sy, sx, ac);
+    if (e0 != cudaSuccess) return e0;
   }
   cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess && amax)
@@ -732,20 +745,20 @@ cudaError_t transpose_t(const void* in, void* out, int N, int C, int HW, bool to
 cudaError_t launch_upsample_add(DType dt, const void* coarse, const void* lat, void* out, int N,
                                 int C, int Hc, int Wc, int H, int W, int align_corners,
                                 Layout layout, cudaStream_t s, unsigned* amax_out,
-                                const MergeScaledCopy* scaled) {
+                                const MergeScaledCopy* scaled, bool pdl) {
   if (scaled && (!scaled->out || !scaled->scale_a || !scaled->scale_w || !aligned16(scaled->out)))
     return cudaErrorInvalidValue;
   switch (dt) {
     case DType::F32:
       if (scaled) return cudaErrorNotSupported;
       return upsample_add_t<float>(coarse, lat, out, N, C, Hc, Wc, H, W, align_corners, layout, s,
-                                   amax_out, nullptr);
+                                   amax_out, nullptr, pdl);
     case DType::F16:
       return upsample_add_t<__half>(coarse, lat, out, N, C, Hc, Wc, H, W, align_corners, layout,
-                                    s, amax_out, scaled);
+                                    s, amax_out, scaled, pdl);
     case DType::BF16:
       return upsample_add_t<__nv_bfloat16>(coarse, lat, out, N, C, Hc, Wc, H, W, align_corners,
-                                           layout, s, amax_out, scaled);
+                                           layout, s, amax_out, scaled, pdl);
     default:
       return cudaErrorInvalidValue;
   }
@@ -831,7 +844,7 @@ cudaError_t launch_absmax(DType dt, const void* x, long long n, int groups, unsi
 
 cudaError_t launch_quantize_e4m3(DType dt, const void* x, long long n, int groups,
                                  const unsigned* amax_bits, void* q, float* scale_out,
-                                 cudaStream_t s) {
+                                 cudaStream_t s, bool pdl) {
   if (n <= 0 || !x || !q || !amax_bits) return cudaErrorInvalidValue;
   if (groups < 1 || groups > 65535 || n % groups != 0) return cudaErrorInvalidValue;
   const long long per = n / groups;
@@ -844,21 +857,17 @@ cudaError_t launch_quantize_e4m3(DType dt, const void* x, long long n, int group
   uint8_t* qb = static_cast<uint8_t*>(q);
   switch (dt) {
     case DType::F32:
-      quantize_e4m3_kernel<float>
-          <<<g, 256, 0, s>>>(static_cast<const float*>(x), n, vec, amax_bits, qb, scale_out);
-      break;
+      return launch_ex(quantize_e4m3_kernel<float>, g, dim3(256), 0, s, pdl, 1,
+                       static_cast<const float*>(x), n, vec, amax_bits, qb, scale_out);
     case DType::F16:
-      quantize_e4m3_kernel<__half>
-          <<<g, 256, 0, s>>>(static_cast<const __half*>(x), n, vec, amax_bits, qb, scale_out);
-      break;
+      return launch_ex(quantize_e4m3_kernel<__half>, g, dim3(256), 0, s, pdl, 1,
+                       static_cast<const __half*>(x), n, vec, amax_bits, qb, scale_out);
     case DType::BF16:
-      quantize_e4m3_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(
-          static_cast<const __nv_bfloat16*>(x), n, vec, amax_bits, qb, scale_out);
-      break;
+      return launch_ex(quantize_e4m3_kernel<__nv_bfloat16>, g, dim3(256), 0, s, pdl, 1,
+                       static_cast<const __nv_bfloat16*>(x), n, vec, amax_bits, qb, scale_out);
     default:
       return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
 }
 
 cudaError_t launch_quantize_rows_e4m3(const float* w, int rows, int cols, int pack_cin, void* q,

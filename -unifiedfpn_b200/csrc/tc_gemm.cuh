@@ -640,6 +640,7 @@ __global__ void __launch_bounds__(TcCfgT<kMode, T>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();  // (programmatic launch) the previous kernel's results are visible
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer (whole warp)
@@ -713,6 +714,7 @@ __global__ void __launch_bounds__(TcCfgT<kMode, T>::kThreads, 1)
         }
       }
     }
+    griddep_launch_dependents();  // this CTA's last loads are issued
     // Teardown: every copy issued must land before the CTA exits (matters only when
     // another role aborted early).
     if (lane == 0) {
@@ -892,6 +894,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();  // (programmatic launch) the previous kernel's results are visible
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -933,6 +936,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
         }
       }
+      griddep_launch_dependents();  // this CTA's last loads are issued
       for (int i = 0; i < S && i < issued; ++i) {
         if (--stage < 0) {
           stage = S - 1;

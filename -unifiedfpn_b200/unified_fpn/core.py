@@ -284,12 +284,18 @@ class UnifiedFPN:
         check(lib.ufpn_core_set_kernel_config(self._h, tile_size, channels_per_thread, int(use_tensor_cores),
                                               _ACT[activation], int(enable_graph_capture)), "set_kernel_config")
 
-    def set_schedule(self, fused_neck_kernel: bool = False, single_stream: bool = False) -> None:
+    def set_schedule(self, fused_neck_kernel: bool = False, single_stream: bool = False,
+                     programmatic_launch: bool = True) -> None:
         """Tensor-core schedule: one persistent kernel for the whole neck, or per-level
-        kernels on two streams (default) or, with ``single_stream``, one after the other on
-        the caller's stream (bitwise the same results as the default)."""
+        kernels on several streams (default) or, with ``single_stream``, one after the other
+        on the caller's stream (bitwise the same results as the default).
+        ``programmatic_launch`` (16-bit split schedule): kernels that follow a kernel on the
+        main stream start during its tail and wait on the device for its results (same
+        results, less launch latency)."""
         mode = 1 if fused_neck_kernel else (2 if single_stream else 0)
         check(lib.ufpn_core_set_schedule(self._h, mode), "set_schedule")
+        check(lib.ufpn_core_set_programmatic_launch(self._h, int(programmatic_launch)),
+              "set_programmatic_launch")
 
     def neck_timeline(self, backbone_features) -> dict:
         """Runs one forward with the fused neck kernel's device timeline recorded and

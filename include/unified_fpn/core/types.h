@@ -143,6 +143,11 @@ struct FPNKernelConfig {
   // Split schedule only: run every kernel on the caller's stream, one after the other
   // (false: each level's 3x3 on a second stream, overlapping the top-down chain).
   bool single_stream = false;
+  // 16-bit split schedule: launch each kernel that follows another kernel on the main
+  // stream as a programmatic dependent launch (it is scheduled during its predecessor's
+  // tail, sets up and waits on the device for the predecessor's results), hiding launch
+  // latency and prologues along the P5 -> P2 chain.  (Not used by the e4m3 schedule.)
+  bool programmatic_launch = true;
 };
 
 struct FPNWeights {

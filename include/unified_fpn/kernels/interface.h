@@ -44,7 +44,7 @@ struct MergeScaledCopy {
 cudaError_t launch_upsample_add(DType dt, const void* coarse, const void* lat, void* out, int N,
                                 int C, int Hc, int Wc, int H, int W, int align_corners,
                                 Layout layout, cudaStream_t s, unsigned* amax_out = nullptr,
-                                const MergeScaledCopy* scaled = nullptr);
+                                const MergeScaledCopy* scaled = nullptr, bool pdl = false);
 // ---- e4m3 quantisation (simt_kernels.cu).  scale = amax / 448, q = e4m3_rn_satfinite(
 // x * (448 / amax)) (amax == 0: scale = 1, q = 0); amax carried as fp32 bits.
 // The n elements form `groups` equal consecutive groups (images), each with its own
@@ -56,7 +56,7 @@ cudaError_t launch_absmax(DType dt, const void* x, long long n, int groups, unsi
 // scales to scale_out[groups] (device, may be null).
 cudaError_t launch_quantize_e4m3(DType dt, const void* x, long long n, int groups,
                                  const unsigned* amax_bits, void* q, float* scale_out,
-                                 cudaStream_t s);
+                                 cudaStream_t s, bool pdl = false);
 // Per-row (output channel) quantisation of fp32 weights [rows][cols] -> e4m3 + scales[rows].
 // pack_cin > 0: rows are [pack_cin][3][3] and q is written [9][pack_cin] (3x3 K order).
 cudaError_t launch_quantize_rows_e4m3(const float* w, int rows, int cols, int pack_cin, void* q,
@@ -206,8 +206,12 @@ struct NeckJobSpec {
 cudaError_t plan_neck_jobs(NeckPlan& plan, DType dt, int N, const NeckLevel* levels, void* p6,
                            const NeckJobSpec* specs, int num_specs, int* sched, int* status,
                            int max_ctas, unsigned long long* trace = nullptr);
-cudaError_t launch_neck(const NeckPlan& plan, cudaStream_t s);
-cudaError_t launch_tc(const TcPlan& plan, cudaStream_t s);
+// pdl (every launcher that takes it): programmatic dependent launch -- the kernel may be
+// scheduled while the previous kernel of stream s still runs; it sets up, then waits for
+// that kernel's completion before touching memory (griddepcontrol.wait).  Only for a launch
+// whose predecessor in the stream is a kernel.
+cudaError_t launch_neck(const NeckPlan& plan, cudaStream_t s, bool pdl = false);
+cudaError_t launch_tc(const TcPlan& plan, cudaStream_t s, bool pdl = false);
 
 // Number of SMs on the current device (cached).
 int sm_count();

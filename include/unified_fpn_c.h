@@ -82,6 +82,10 @@ int ufpn_core_set_kernel_config(ufpn_core* core, int tile_size, int channels_per
  * No reference counterpart (its engine launched 16 kernels on four unordered streams,
  * fpn_engine.cu:191-245). */
 int ufpn_core_set_schedule(ufpn_core* core, int fused_neck_kernel);
+/* 16-bit split schedule: 1 (default) = kernels that follow a kernel on the main stream are
+ * programmatic dependent launches (scheduled during the predecessor's tail, waiting on the
+ * device for its results); 0 = ordinary stream order.  Results are the same either way. */
+int ufpn_core_set_programmatic_launch(ufpn_core* core, int enable);
 /* fpn_engine.cu:408-415 (get_memory_usage) */
 size_t ufpn_core_get_memory_usage(const ufpn_core* core);
 /* fpn_pytorch.cpp:171-187 (get_performance_breakdown): kernel_times_ms[8], metrics[5] =
