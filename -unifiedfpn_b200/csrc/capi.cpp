@@ -224,11 +224,14 @@ int ufpn_core_set_schedule(ufpn_core* core, int fused_neck_kernel) {
   });
 }
 
-int ufpn_core_set_programmatic_launch(ufpn_core* core, int enable) {
+int ufpn_core_set_schedule_options(ufpn_core* core, int programmatic_launch, int chain_priority,
+                                   int merge_two_levels) {
   if (!core) return fail(UFPN_ERR_INVALID_ARG, "NULL core");
   return guarded([&] {
     FPNKernelConfig c = core->core.get_kernel_config();
-    c.programmatic_launch = enable != 0;
+    c.programmatic_launch = programmatic_launch != 0;
+    c.chain_priority = chain_priority != 0;
+    c.merge_two_levels = merge_two_levels != 0;
     core->core.set_kernel_config(c);
     return UFPN_OK;
   });
@@ -378,6 +381,23 @@ int ufpn_upsample_add(int dtype, int layout, const void* coarse, const void* lat
   cudaError_t e = ufpn::launch_upsample_add(dt, coarse, lateral, out, N, C, Hc, Wc, H, W,
                                             align_corners, lay, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "upsample_add");
+}
+
+int ufpn_merge_two_levels(int dtype, const void* m5, const void* l4, void* m4, void* l3_m3, int N,
+                          int H5, int W5, int H4, int W4, int H3, int W3, void* stream) {
+  DType dt;
+  if (!parse_dtype(dtype, &dt)) return fail(UFPN_ERR_UNSUPPORTED, "unsupported dtype");
+  if (dt != DType::BF16 && dt != DType::F16)
+    return fail(UFPN_ERR_UNSUPPORTED, "two-level merge: bf16 or fp16 maps");
+  if (!m5 || !l4 || !m4 || !l3_m3) return fail(UFPN_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (l4 == m4) return fail(UFPN_ERR_INVALID_ARG, "l4 must not alias m4");
+  if (N <= 0 || H5 <= 0 || W5 <= 0 || H4 <= 0 || W4 <= 0 || H3 <= 0 || W3 <= 0)
+    return fail(UFPN_ERR_INVALID_ARG, "sizes must be positive");
+  if (H5 > H4 || W5 > W4 || H4 > H3 || W4 > W3)
+    return fail(UFPN_ERR_UNSUPPORTED, "two-level merge: each map must upsample to the next");
+  cudaError_t e = ufpn::launch_merge_two_levels(dt, m5, l4, m4, l3_m3, l3_m3, N, H5, W5, H4, W4,
+                                                H3, W3, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "merge_two_levels");
 }
 
 int ufpn_p6_maxpool(int dtype, int layout, const void* p5, void* p6, int N, int C, int H, int W,

@@ -104,6 +104,9 @@ struct UnifiedFPNCore::Impl {
   void* merged[4] = {};   // M_l in the compute dtype (bf16 for e4m3 inputs)
   void* qmerged[4] = {};  // e4m3: M_l quantised per image (input of the 3x3)
   void* m3_scaled = nullptr;  // e4m3: M3 / (scale(C2) * lateral-P2 weight scale), per channel
+  // Raw P4 lateral L4 when the P4 and P3 merges run as one launch (which reads L4 around
+  // each tile while it writes M4, so L4 cannot be merged in place); null: merge per level.
+  void* lat4_raw = nullptr;
   void* wb_table = nullptr;   // P2 lateral's precomputed top-down (bilinear) weights
   const float* in_scale[4] = {};  // e4m3: scales of the current forward's inputs
   unsigned* fp8_amax = nullptr;   // e4m3: [4][N] per-image absmax of M_l (fp32 bits)
@@ -126,6 +129,7 @@ struct UnifiedFPNCore::Impl {
   cudaEvent_t ev_lat[4] = {};
   cudaEvent_t ev_join = nullptr;
   cudaEvent_t ev_join_lat[2] = {};  // joins of the P4 / P3 3x3 streams
+  int chain_priority_value = 0;     // greatest launch priority of the device
   cudaEvent_t prof[10] = {};
   FPNKernelConfig cfg;
   Conv3x3Tiling tiling[4];
@@ -165,6 +169,8 @@ struct UnifiedFPNCore::Impl {
     fp8_scale = nullptr;
     cudaFree(m3_scaled);
     m3_scaled = nullptr;
+    cudaFree(lat4_raw);
+    lat4_raw = nullptr;
     cudaFree(wb_table);
     wb_table = nullptr;
     workspace_bytes = 0;
@@ -364,12 +370,21 @@ struct UnifiedFPNCore::Impl {
     // Programmatic dependent launches for every kernel that follows a kernel of ours on its
     // stream (not under profiling events, which time kernels one by one).
     const bool pdl = !prof_events && cfg.programmatic_launch;
+    // Launch options of the main-stream chain: programmatic launches, and (chain_priority) a
+    // higher priority than the side streams' 3x3s, so that SMs freed while the chain's next
+    // kernel waits for them go to it rather than to a side 3x3.
+    ufpn::LaunchOpts chain;
+    chain.pdl = pdl;
+    chain.priority = cfg.chain_priority ? chain_priority_value : 0;
+    ufpn::LaunchOpts chain_first = chain;  // first kernel of the forward: no kernel before it
+    chain_first.pdl = false;
     // Main stream (the top-down data dependence):
     //   1. ONE grouped launch of the raw P5, P4, P3 laterals L5, L4, L3 (as GEMMs they do
     //      not depend on one another; only their top-down adds chain);
-    //   2. in-place merges M4 = L4 + up(M5), M3 = L3 + up(M4) (bandwidth kernels on the
-    //      small maps; M5 = L5);
-    //   3. the P2 lateral with the top-down add of M3 fused into its epilogue.
+    //   2. the merges M4 = L4 + up(M5), M3 = L3 + up(M4) (M5 = L5): one bandwidth kernel
+    //      for both when the maps upsample (merge_two_levels; L4 then sits in lat4_raw),
+    //      else two in-place merges;
+    //   3. the P2 lateral with the top-down add of M3 through its tensor-core k-block.
     // Side streams, one per level: the P5, P4 and P3 3x3s, each as soon as its merged map
     // exists, so the small P5 / P4 grids run beside the chain instead of one after the
     // other; the P2 3x3 follows the P2 lateral on the main stream.
@@ -401,25 +416,43 @@ struct UnifiedFPNCore::Impl {
             "plan conv3x3");
       // (on the main stream the 3x3 follows a kernel: the P2 lateral, or the previous
       // level's merge / 3x3 when every kernel runs on one stream)
-      ok(ufpn::launch_tc(conv, st, pdl && st == main), "conv3x3 launch");
+      ok(ufpn::launch_tc(conv, st, st == main ? chain : ufpn::LaunchOpts()), "conv3x3 launch");
     };
+    // With lat4_raw: L4 goes there and ONE launch merges M4 and M3 (merge_two_levels).
+    const bool two_level = lat4_raw != nullptr && cfg.merge_two_levels;
+    if (two_level) lv[2].merged = lat4_raw;
     const ufpn::NeckJobSpec grouped[3] = {{0, 3, 0}, {0, 2, 0}, {0, 1, 0}};
     ufpn::NeckPlan gplan;
     check(ufpn::plan_neck_jobs(gplan, dtype, batch, lv, nullptr, grouped, 3, d_sched, d_status, 0,
                                trace_next ? d_trace : nullptr),
           "plan grouped laterals");
-    ok(ufpn::launch_neck(gplan, main), "grouped laterals launch");
+    ok(ufpn::launch_neck(gplan, main, nchw ? chain : chain_first), "grouped laterals launch");
     if (prof_events) cudaEventRecord(prof[1], main);
     conv_level(3);
     if (prof_events) cudaEventRecord(prof[2], main);
-    for (int l = 2; l >= 1; --l) {
-      ok(ufpn::launch_upsample_add(dtype, merged[l + 1], merged[l], merged[l], batch, cout,
-                                   H[l + 1], W[l + 1], H[l], W[l], 0, Layout::NHWC, main, nullptr,
-                                   nullptr, pdl),
-         "merge");
-      if (prof_events) cudaEventRecord(prof[3 + 2 * (2 - l)], main);
-      conv_level(l);
-      if (prof_events) cudaEventRecord(prof[4 + 2 * (2 - l)], main);
+    if (two_level) {
+      ok(ufpn::launch_merge_two_levels(dtype, merged[3], lat4_raw, merged[2], merged[1],
+                                       merged[1], batch, H[3], W[3], H[2], W[2], H[1], W[1],
+                                       main, nullptr, nullptr, nullptr, chain),
+         "merge P4 and P3");
+      if (prof_events) cudaEventRecord(prof[3], main);
+      conv_level(2);
+      if (prof_events) {
+        cudaEventRecord(prof[4], main);
+        cudaEventRecord(prof[5], main);  // (no separate P3 merge)
+      }
+      conv_level(1);
+      if (prof_events) cudaEventRecord(prof[6], main);
+    } else {
+      for (int l = 2; l >= 1; --l) {
+        ok(ufpn::launch_upsample_add(dtype, merged[l + 1], merged[l], merged[l], batch, cout,
+                                     H[l + 1], W[l + 1], H[l], W[l], 0, Layout::NHWC, main,
+                                     nullptr, nullptr, chain),
+           "merge");
+        if (prof_events) cudaEventRecord(prof[3 + 2 * (2 - l)], main);
+        conv_level(l);
+        if (prof_events) cudaEventRecord(prof[4 + 2 * (2 - l)], main);
+      }
     }
     TcPlan lat2;
     check(ufpn::plan_tc_lateral(lat2, dtype, x[0], lat_wp[0], lat_b[0], merged[1], merged[0],
@@ -427,7 +460,7 @@ struct UnifiedFPNCore::Impl {
                                 0),
           "plan lateral");
     ufpn::tc_attach_wb_table(lat2, wb_table);
-    ok(ufpn::launch_tc(lat2, main, pdl), "lateral launch");
+    ok(ufpn::launch_tc(lat2, main, chain), "lateral launch");
     if (prof_events) cudaEventRecord(prof[7], main);
     conv_level(0);
     if (prof_events) cudaEventRecord(prof[8], main);
@@ -464,10 +497,12 @@ struct UnifiedFPNCore::Impl {
   // writes it (P5 / P2 lateral epilogue, P4 / P3 merge) and is quantised to e4m3 per image
   // on its 3x3's stream right before the 3x3 (per image, so an image's result does not
   // depend on the rest of its batch, e.g. on how a batch is sharded over GPUs):
-  //   main:        zero amax | lat5 (amax5) | merge4 (amax4) | merge3 (amax3, M3s) | lat2 + up(M3s) (amax2) | q2 3x3_2
+  //   main:        zero amax | lat5 (amax5) | merge4 + merge3 (amax4, amax3, M3s) | lat2 + up(M3s) (amax2) | q2 3x3_2
   //   side:                                  q5 3x3_5 (+P6)
-  //   lat_side[0]:             lat4                            q4 3x3_4
-  //   lat_side[1]:             lat3                                                 q3 3x3_3
+  //   lat_side[0]:             lat4                                                q4 3x3_4
+  //   lat_side[1]:             lat3                                                q3 3x3_3
+  // (the two merges are one launch when the maps upsample -- merge_two_levels, L4 from
+  // lat4_raw -- else two in-place merges with q4 3x3_4 between them)
   int enqueue_e4m3(const void* const* in, void* const* out, void* p6, cudaStream_t main,
                    bool prof_events) {
     int launches = 0;
@@ -480,6 +515,12 @@ struct UnifiedFPNCore::Impl {
     // batch-16 workload (its quantisation kernels release their dependents at their start,
     // so the next 3x3's CTAs wait on SMs the other streams could use): off.
     const bool pdl = false;
+    auto opts = [](bool p) {
+      ufpn::LaunchOpts o;
+      o.pdl = p;
+      return o;
+    };
+    const bool two_level = lat4_raw != nullptr && cfg.merge_two_levels;
     if (prof_events) cudaEventRecord(prof[0], main);
     check(cudaMemsetAsync(fp8_amax, 0, 4 * static_cast<size_t>(batch) * sizeof(unsigned), main),
           "memset");
@@ -495,13 +536,15 @@ struct UnifiedFPNCore::Impl {
       sc.amax_out = amax_out;
       sc.coarse_prescaled = coarse != nullptr;  // coarse = m3_scaled
       TcPlan p;
-      check(ufpn::plan_tc_lateral(p, DType::E4M3, in[l], lat_wp[l], lat_b[l], coarse, merged[l],
+      // (with lat4_raw, L4 goes there: the two-level merge writes M4)
+      void* lout = (l == 2 && two_level) ? lat4_raw : merged[l];
+      check(ufpn::plan_tc_lateral(p, DType::E4M3, in[l], lat_wp[l], lat_b[l], coarse, lout,
                                   batch, cin[l], H[l], W[l], coarse ? H[l + 1] : 0,
                                   coarse ? W[l + 1] : 0, ufpn::default_tiling(H[l], W[l]),
                                   d_status, 0, sc),
             "plan e4m3 lateral");
       if (l == 0) ufpn::tc_attach_wb_table(p, wb_table);
-      ok(ufpn::launch_tc(p, st, pdl && after_kernel), "e4m3 lateral launch");
+      ok(ufpn::launch_tc(p, st, opts(pdl && after_kernel)), "e4m3 lateral launch");
     };
     // quantise = false: qmerged[l] and its scales were written by the kernel producing M_l.
     auto conv_level = [&](int l, bool quantise = true) {
@@ -524,7 +567,7 @@ struct UnifiedFPNCore::Impl {
       if (quantise && !in_kernel)
         ok(ufpn::launch_quantize_e4m3(DType::BF16, merged[l], n, batch, fp8_amax + l * batch,
                                       qmerged[l], fp8_scale + l * batch, conv_st,
-                                      pdl && conv_st == main),
+                                      opts(pdl && conv_st == main)),
            "quantise merged map");
       ufpn::TcScales sc;
       sc.ascale = fp8_scale + l * batch;
@@ -536,7 +579,8 @@ struct UnifiedFPNCore::Impl {
                                   out_wp[l], out_b[l], out[l], l == 3 ? p6 : nullptr, batch,
                                   H[l], W[l], t, d_status, 0, sc),
             "plan e4m3 conv3x3");
-      ok(ufpn::launch_tc(conv, conv_st, pdl && (conv_st == main || (quantise && !in_kernel))),
+      ok(ufpn::launch_tc(conv, conv_st,
+                         opts(pdl && (conv_st == main || (quantise && !in_kernel)))),
          "e4m3 conv3x3 launch");
     };
     // The three raw laterals are independent GEMMs: P5 on the main stream, P4 and P3 on
@@ -550,21 +594,39 @@ struct UnifiedFPNCore::Impl {
     if (prof_events) cudaEventRecord(prof[1], main);
     conv_level(3);
     if (prof_events) cudaEventRecord(prof[2], main);
-    for (int l = 2; l >= 1; --l) {
-      if (!one_stream) check(cudaStreamWaitEvent(main, ev_lat_done[2 - l], 0), "event");
-      // M3 also gets its copy pre-divided by the P2 lateral's per-channel scale, which the P2
-      // lateral adds through its tensor-core top-down k-block.
-      ufpn::MergeScaledCopy m3s;
-      m3s.out = m3_scaled;
-      m3s.scale_a = in_scale[0];
-      m3s.scale_w = lat_ws[0];
-      ok(ufpn::launch_upsample_add(DType::BF16, merged[l + 1], merged[l], merged[l], batch, cout,
-                                   H[l + 1], W[l + 1], H[l], W[l], 0, Layout::NHWC, main,
-                                   fp8_amax + l * batch, l == 1 ? &m3s : nullptr, pdl),
-         "merge");
-      if (prof_events) cudaEventRecord(prof[3 + 2 * (2 - l)], main);
-      conv_level(l);
-      if (prof_events) cudaEventRecord(prof[4 + 2 * (2 - l)], main);
+    // M3 also gets its copy pre-divided by the P2 lateral's per-channel scale, which the P2
+    // lateral adds through its tensor-core top-down k-block.
+    ufpn::MergeScaledCopy m3s;
+    m3s.out = m3_scaled;
+    m3s.scale_a = in_scale[0];
+    m3s.scale_w = lat_ws[0];
+    if (two_level) {
+      if (!one_stream)
+        for (int i = 0; i < 2; ++i) check(cudaStreamWaitEvent(main, ev_lat_done[i], 0), "event");
+      ok(ufpn::launch_merge_two_levels(DType::BF16, merged[3], lat4_raw, merged[2], merged[1],
+                                       merged[1], batch, H[3], W[3], H[2], W[2], H[1], W[1],
+                                       main, fp8_amax + 2 * batch, fp8_amax + batch, &m3s,
+                                       opts(pdl)),
+         "merge P4 and P3");
+      if (prof_events) cudaEventRecord(prof[3], main);
+      conv_level(2);
+      if (prof_events) {
+        cudaEventRecord(prof[4], main);
+        cudaEventRecord(prof[5], main);  // (no separate P3 merge)
+      }
+      conv_level(1);
+      if (prof_events) cudaEventRecord(prof[6], main);
+    } else {
+      for (int l = 2; l >= 1; --l) {
+        if (!one_stream) check(cudaStreamWaitEvent(main, ev_lat_done[2 - l], 0), "event");
+        ok(ufpn::launch_upsample_add(DType::BF16, merged[l + 1], merged[l], merged[l], batch,
+                                     cout, H[l + 1], W[l + 1], H[l], W[l], 0, Layout::NHWC, main,
+                                     fp8_amax + l * batch, l == 1 ? &m3s : nullptr, opts(pdl)),
+           "merge");
+        if (prof_events) cudaEventRecord(prof[3 + 2 * (2 - l)], main);
+        conv_level(l);
+        if (prof_events) cudaEventRecord(prof[4 + 2 * (2 - l)], main);
+      }
     }
     lateral(0, m3_scaled, fp8_amax, main, true);
     if (prof_events) cudaEventRecord(prof[7], main);
@@ -601,6 +663,11 @@ UnifiedFPNCore::UnifiedFPNCore(size_t workspace_size, int device) : impl_(new Im
   impl_->workspace_cap = workspace_size;
   DeviceGuard g(device);
   CUDA_CHECK(cudaStreamCreateWithFlags(&impl_->side, cudaStreamNonBlocking));
+  {
+    int least = 0, greatest = 0;
+    CUDA_CHECK(cudaDeviceGetStreamPriorityRange(&least, &greatest));
+    impl_->chain_priority_value = greatest;
+  }
   CUDA_CHECK(cudaStreamCreateWithFlags(&impl_->capture, cudaStreamNonBlocking));
   CUDA_CHECK(cudaStreamCreateWithFlags(&impl_->setup, cudaStreamNonBlocking));
   for (int i = 0; i < 2; ++i) {
@@ -685,6 +752,12 @@ void UnifiedFPNCore::configure_levels(const std::vector<FPNDimensions>& dims, in
       m.check(cudaMalloc(&m.nhwc_out[l], px * m.cout * esz), "workspace");
       total += px * (m.cin[l] + m.cout) * esz;
     }
+  }
+  if (m.tensor_core_path() && m.cfg.merge_two_levels && m.cout == 256 && m.H[3] <= m.H[2] &&
+      m.W[3] <= m.W[2] && m.H[2] <= m.H[1] && m.W[2] <= m.W[1]) {
+    const size_t px4 = static_cast<size_t>(N) * m.H[2] * m.W[2];
+    m.check(cudaMalloc(&m.lat4_raw, px4 * m.cout * msz), "workspace");
+    total += px4 * m.cout * msz;
   }
   if (m.tensor_core_path()) {
     // The P2 lateral's top-down weights depend only on the geometry: build them once.
@@ -859,7 +932,9 @@ void UnifiedFPNCore::forward_raw_scaled(const void* const* in, const float* cons
     }
     m.check(cudaStreamEndCapture(m.capture, &graph), "capture");
     cudaGraphExec_t exec = nullptr;
-    const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+    // Per-node priorities (the main-stream chain's launch priority) hold only when asked for.
+    const cudaError_t ie =
+        cudaGraphInstantiate(&exec, graph, cudaGraphInstantiateFlagUseNodePriority);
     cudaGraphDestroy(graph);
     m.check(ie, "cudaGraphInstantiate");
     if (m.graphs.size() >= 8) {

@@ -280,6 +280,176 @@ __global__ void __launch_bounds__(256) upsample_add_px512_kernel(
   if (amax && m_img >= 0) publish_amax_block(amax + m_img, m, red);
 }
 
+// ---------------------------------------------------------------- two-level merge
+// M4 = L4 + up(M5) and M3 = L3 + up(M4) in ONE launch (NHWC, 256 channels of a 16-bit type,
+// maps that upsample).  A block owns a kMergeTileH x kMergeTileW tile of M3 and
+//   1. computes into shared memory every M4 pixel its tile's taps read, from L4 and four M5
+//      taps, rounded to T exactly as the M4 map stores it; the M4 pixels it owns (the
+//      rectangle [y0 H4 / H3, y1 H4 / H3) x [x0 W4 / W3, x1 W4 / W3), integer division, for
+//      tile rows [y0, y1) and columns [x0, x1): these rectangles partition M4) also go to m4;
+//   2. computes its M3 pixels from L3 (in place) and the shared M4 pixels.
+// The arithmetic is that of two upsample_add_px512 passes (same taps, weights and fmaf
+// order, one rounding per map), so the results are bitwise the same; the second pass's
+// reads of M4 and the launch boundary between the passes disappear.  l4 must not alias m4
+// (a block reads L4 pixels its neighbours own); l3 may alias m3.  The region computed in
+// step 1 is the union of the tap rows / columns and the owned rectangle; reg_h x reg_w
+// bounds it (host) and sizes the dynamic shared memory.
+// Optional as in upsample_add_px512: amax4[n] / amax3[n] (|M4|, |M3| of image n, fp32 bits)
+// and m3s, a copy of M3 with channel c scaled by 1 / (scale_a[0] * scale_w[c]).
+constexpr int kMergeTileH = 8;
+constexpr int kMergeTileW = 16;
+template <typename T>
+__global__ void __launch_bounds__(256, 3) merge_two_levels_kernel(
+    const T* __restrict__ m5, const T* __restrict__ l4, T* __restrict__ m4, const T* l3, T* m3,
+    int H5, int W5, int H4, int W4, int H3, int W3, float s54y, float s54x, float s43y,
+    float s43x, int tiles_x, int tiles_y, int reg_h, int reg_w, unsigned* amax4,
+    unsigned* amax3, T* m3s, const float* scale_a, const float* scale_w) {
+  static_assert(sizeof(T) == 2, "16-bit types");
+  griddep_wait();  // (programmatic launch) inputs written by the previous kernel
+  griddep_launch_dependents();
+  extern __shared__ uint4 merge_smem[];  // [reg_h * reg_w pixels][32 lanes] x 16 bytes
+  __shared__ unsigned red[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tx = static_cast<int>(blockIdx.x) % tiles_x;
+  const int t2 = static_cast<int>(blockIdx.x) / tiles_x;
+  const int ty = t2 % tiles_y;
+  const int n = t2 / tiles_y;
+  const int y0 = ty * kMergeTileH, x0 = tx * kMergeTileW;
+  const int y1 = min(y0 + kMergeTileH, H3), x1 = min(x0 + kMergeTileW, W3);  // exclusive
+  // owned M4 rectangle
+  const int oy0 = static_cast<int>(static_cast<long long>(y0) * H4 / H3);
+  const int oy1 = static_cast<int>(static_cast<long long>(y1) * H4 / H3);
+  const int ox0 = static_cast<int>(static_cast<long long>(x0) * W4 / W3);
+  const int ox1 = static_cast<int>(static_cast<long long>(x1) * W4 / W3);
+  // region: tap rows / columns of the tile's pixels, united with the owned rectangle
+  const int ry0 = min(static_cast<int>(src_coord(y0, H4, H3, s43y, 0)), oy0);
+  const int ry1 = max(min(static_cast<int>(src_coord(y1 - 1, H4, H3, s43y, 0)) + 1, H4 - 1),
+                      oy1 - 1);
+  const int rx0 = min(static_cast<int>(src_coord(x0, W4, W3, s43x, 0)), ox0);
+  const int rx1 = max(min(static_cast<int>(src_coord(x1 - 1, W4, W3, s43x, 0)) + 1, W4 - 1),
+                      ox1 - 1);
+  const int rh = ry1 - ry0 + 1, rw = rx1 - rx0 + 1;
+  if (rh > reg_h || rw > reg_w) return;  // cannot happen for the host's bound (uniform exit)
+
+  unsigned m = 0;
+  // ---- 1. M4 region, kB pixels per warp at a time (all their loads issued first)
+  constexpr int kB = 2;
+  const T* m5n = m5 + static_cast<size_t>(n) * H5 * W5 * 256 + lane * 8;
+  for (int i0 = warp; i0 < rh * rw; i0 += 8 * kB) {
+    Vec16<T> l[kB], a[kB], b[kB], c[kB], d[kB];
+    float wy[kB], wx[kB];
+#pragma unroll
+    for (int k = 0; k < kB; ++k) {
+      const int i = min(i0 + 8 * k, rh * rw - 1);  // clamped duplicates are not stored
+      const int yy = ry0 + i / rw, xx = rx0 + i % rw;
+      const float sy = src_coord(yy, H5, H4, s54y, 0);
+      const float sx = src_coord(xx, W5, W4, s54x, 0);
+      const int ya = static_cast<int>(sy), xa = static_cast<int>(sx);
+      const int yb = min(ya + 1, H5 - 1), xb = min(xa + 1, W5 - 1);
+      wy[k] = sy - static_cast<float>(ya);
+      wx[k] = sx - static_cast<float>(xa);
+      const size_t io = (static_cast<size_t>(n * H4 + yy) * W4 + xx) * 256 + lane * 8;
+      l[k].u = __ldg(reinterpret_cast<const uint4*>(l4 + io));
+      a[k].u = __ldg(reinterpret_cast<const uint4*>(m5n + (static_cast<size_t>(ya) * W5 + xa) * 256));
+      b[k].u = __ldg(reinterpret_cast<const uint4*>(m5n + (static_cast<size_t>(ya) * W5 + xb) * 256));
+      c[k].u = __ldg(reinterpret_cast<const uint4*>(m5n + (static_cast<size_t>(yb) * W5 + xa) * 256));
+      d[k].u = __ldg(reinterpret_cast<const uint4*>(m5n + (static_cast<size_t>(yb) * W5 + xb) * 256));
+    }
+#pragma unroll
+    for (int k = 0; k < kB; ++k) {
+      const int i = i0 + 8 * k;
+      if (i >= rh * rw) break;
+      const int yy = ry0 + i / rw, xx = rx0 + i % rw;
+      const float w00 = (1.f - wy[k]) * (1.f - wx[k]), w01 = (1.f - wy[k]) * wx[k];
+      const float w10 = wy[k] * (1.f - wx[k]), w11 = wy[k] * wx[k];
+      Vec16<T> o;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float v = to_f(l[k].e[e]);
+        v = fmaf(to_f(a[k].e[e]), w00, v);
+        v = fmaf(to_f(b[k].e[e]), w01, v);
+        v = fmaf(to_f(c[k].e[e]), w10, v);
+        v = fmaf(to_f(d[k].e[e]), w11, v);
+        o.e[e] = from_f<T>(v);
+      }
+      merge_smem[i * 32 + lane] = o.u;
+      if (yy >= oy0 && yy < oy1 && xx >= ox0 && xx < ox1) {
+        const size_t io = (static_cast<size_t>(n * H4 + yy) * W4 + xx) * 256 + lane * 8;
+        *reinterpret_cast<uint4*>(m4 + io) = o.u;
+        if (amax4) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) m = max(m, abs_bits(to_f(o.e[e])));
+        }
+      }
+    }
+  }
+  if (amax4) publish_amax_block(amax4 + n, m, red);  // (also orders the shared M4 writes)
+  else __syncthreads();
+
+  // ---- 2. M3 tile
+  float inv[8];
+  if (m3s) {
+    const float sa = __ldg(scale_a);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) inv[e] = __frcp_rn(sa * __ldg(scale_w + lane * 8 + e));
+  }
+  m = 0;
+  // the warp's pixels kPx at a time: their L3 loads first (each pixel is read, then
+  // written, by the same lane, so an in-place M3 is safe), then the taps and the stores
+  constexpr int kPx = 8;
+#pragma unroll 1
+  for (int p0 = warp; p0 < kMergeTileH * kMergeTileW; p0 += 8 * kPx) {
+  Vec16<T> lt[kPx];
+#pragma unroll
+  for (int k = 0; k < kPx; ++k) {
+    const int p = p0 + 8 * k;
+    const int y = y0 + p / kMergeTileW, x = x0 + p % kMergeTileW;
+    if (y < y1 && x < x1)
+      lt[k].u = *reinterpret_cast<const uint4*>(
+          l3 + (static_cast<size_t>(n * H3 + y) * W3 + x) * 256 + lane * 8);
+  }
+#pragma unroll
+  for (int k = 0; k < kPx; ++k) {
+    const int p = p0 + 8 * k;
+    const int y = y0 + p / kMergeTileW, x = x0 + p % kMergeTileW;
+    if (y >= y1 || x >= x1) continue;
+    const float sy = src_coord(y, H4, H3, s43y, 0);
+    const float sx = src_coord(x, W4, W3, s43x, 0);
+    const int ya = static_cast<int>(sy), xa = static_cast<int>(sx);
+    const int yb = min(ya + 1, H4 - 1), xb = min(xa + 1, W4 - 1);
+    const float wy = sy - static_cast<float>(ya), wx = sx - static_cast<float>(xa);
+    const size_t io = (static_cast<size_t>(n * H3 + y) * W3 + x) * 256 + lane * 8;
+    Vec16<T> a, b, c, d;
+    const Vec16<T>& l = lt[k];
+    a.u = merge_smem[((ya - ry0) * rw + (xa - rx0)) * 32 + lane];
+    b.u = merge_smem[((ya - ry0) * rw + (xb - rx0)) * 32 + lane];
+    c.u = merge_smem[((yb - ry0) * rw + (xa - rx0)) * 32 + lane];
+    d.u = merge_smem[((yb - ry0) * rw + (xb - rx0)) * 32 + lane];
+    const float w00 = (1.f - wy) * (1.f - wx), w01 = (1.f - wy) * wx;
+    const float w10 = wy * (1.f - wx), w11 = wy * wx;
+    Vec16<T> o;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float v = to_f(l.e[e]);
+      v = fmaf(to_f(a.e[e]), w00, v);
+      v = fmaf(to_f(b.e[e]), w01, v);
+      v = fmaf(to_f(c.e[e]), w10, v);
+      v = fmaf(to_f(d.e[e]), w11, v);
+      o.e[e] = from_f<T>(v);
+      m = max(m, abs_bits(to_f(o.e[e])));
+    }
+    *reinterpret_cast<uint4*>(m3 + io) = o.u;
+    if (m3s) {
+      Vec16<T> os;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) os.e[e] = from_f<T>(to_f(o.e[e]) * inv[e]);
+      *reinterpret_cast<uint4*>(m3s + io) = os.u;
+    }
+  }
+  }
+  if (amax3) publish_amax_block(amax3 + n, m, red);
+}
+
 // ---------------------------------------------------------------- NCHW upsample-add
 // One thread per output element; consecutive threads walk x of one plane.
 template <typename T>
@@ -647,7 +817,7 @@ cudaError_t absmax_t(const void* x, long long n, int groups, unsigned* amax, cud
 template <typename T>
 cudaError_t upsample_add_t(const void* coarse, const void* lat, void* out, int N, int C, int Hc,
                            int Wc, int H, int W, int ac, Layout layout, cudaStream_t s,
-                           unsigned* amax, const MergeScaledCopy* sc, bool pdl) {
+                           unsigned* amax, const MergeScaledCopy* sc, LaunchOpts opts) {
   const float sy = (ac && H > 1) ? static_cast<float>(Hc - 1) / (H - 1)
                                  : static_cast<float>(Hc) / H;
   const float sx = (ac && W > 1) ? static_cast<float>(Wc - 1) / (W - 1)
@@ -674,7 +844,7 @@ cudaError_t upsample_add_t(const void* coarse, const void* lat, void* out, int N
           per = static_cast<int>((blocks + g - 1) / g);
           grid = static_cast<int>((blocks + per - 1) / per);
         }
-        return launch_ex(upsample_add_px512_kernel<T>, dim3(grid), dim3(256), 0, s, pdl, 1, c, l,
+        return launch_ex(upsample_add_px512_kernel<T>, dim3(grid), dim3(256), 0, s, opts, 1, c, l,
                          o, N, Hc, Wc, H, W, chunks, sy, sx, ac, amax,
                          sc ? static_cast<T*>(sc->out) : nullptr, sc ? sc->scale_a : nullptr,
                          sc ? sc->scale_w : nullptr, per);
@@ -686,17 +856,17 @@ cudaError_t upsample_add_t(const void* coarse, const void* lat, void* out, int N
     const int grid = units < 148 * 64 ? static_cast<int>(units) : 148 * 64;
     cudaError_t e0;
     if (vec)
-      e0 = launch_ex(upsample_add_nhwc_kernel<T, true>, dim3(grid), dim3(256), 0, s, pdl, 1, c, l,
+      e0 = launch_ex(upsample_add_nhwc_kernel<T, true>, dim3(grid), dim3(256), 0, s, opts, 1, c, l,
                      o, N, C, Hc, Wc, H, W, sy, sx, ac);
     else
-      e0 = launch_ex(upsample_add_nhwc_kernel<T, false>, dim3(grid), dim3(256), 0, s, pdl, 1, c,
+      e0 = launch_ex(upsample_add_nhwc_kernel<T, false>, dim3(grid), dim3(256), 0, s, opts, 1, c,
                      l, o, N, C, Hc, Wc, H, W, sy, sx, ac);
     if (e0 != cudaSuccess) return e0;
   } else {
     const long long work = static_cast<long long>(N) * C * H * W;
     if (sc) return cudaErrorNotSupported;
     cudaError_t e0 = launch_ex(upsample_add_nchw_kernel<T>, dim3(grid_for(work, 256)), dim3(256),
-                               0, s, pdl, 1, c, l, o, N, C, Hc, Wc, H, W, sy, sx, ac);
+                               0, s, opts, 1, c, l, o, N, C, Hc, Wc, H, W, sy, sx, ac);
     if (e0 != cudaSuccess) return e0;
   }
   cudaError_t e = cudaGetLastError();
@@ -745,23 +915,84 @@ cudaError_t transpose_t(const void* in, void* out, int N, int C, int HW, bool to
 cudaError_t launch_upsample_add(DType dt, const void* coarse, const void* lat, void* out, int N,
                                 int C, int Hc, int Wc, int H, int W, int align_corners,
                                 Layout layout, cudaStream_t s, unsigned* amax_out,
-                                const MergeScaledCopy* scaled, bool pdl) {
+                                const MergeScaledCopy* scaled, LaunchOpts opts) {
   if (scaled && (!scaled->out || !scaled->scale_a || !scaled->scale_w || !aligned16(scaled->out)))
     return cudaErrorInvalidValue;
   switch (dt) {
     case DType::F32:
       if (scaled) return cudaErrorNotSupported;
       return upsample_add_t<float>(coarse, lat, out, N, C, Hc, Wc, H, W, align_corners, layout, s,
-                                   amax_out, nullptr, pdl);
+                                   amax_out, nullptr, opts);
     case DType::F16:
       return upsample_add_t<__half>(coarse, lat, out, N, C, Hc, Wc, H, W, align_corners, layout,
-                                    s, amax_out, scaled, pdl);
+                                    s, amax_out, scaled, opts);
     case DType::BF16:
       return upsample_add_t<__nv_bfloat16>(coarse, lat, out, N, C, Hc, Wc, H, W, align_corners,
-                                           layout, s, amax_out, scaled, pdl);
+                                           layout, s, amax_out, scaled, opts);
     default:
       return cudaErrorInvalidValue;
   }
+}
+
+namespace {
+template <typename T>
+cudaError_t merge_two_levels_t(const void* m5, const void* l4, void* m4, const void* l3, void* m3,
+                               int N, int H5, int W5, int H4, int W4, int H3, int W3,
+                               cudaStream_t s, unsigned* amax4, unsigned* amax3,
+                               const MergeScaledCopy* sc, const LaunchOpts& opts) {
+  // Region bound: the union of a tile's tap rows and its owned M4 rows spans at most
+  // kMergeTileH * H4 / H3 + 3 rows (likewise columns); +4 keeps a margin for rounding.
+  const int reg_h = static_cast<int>(static_cast<long long>(kMergeTileH) * H4 / H3) + 4;
+  const int reg_w = static_cast<int>(static_cast<long long>(kMergeTileW) * W4 / W3) + 4;
+  const size_t smem = static_cast<size_t>(reg_h) * reg_w * 512;
+  if (smem > 200 * 1024) return cudaErrorNotSupported;
+  static size_t configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && configured[dev] < smem) {
+    cudaError_t e = cudaFuncSetAttribute(merge_two_levels_kernel<T>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    configured[dev] = smem;
+  }
+  const int tiles_x = (W3 + kMergeTileW - 1) / kMergeTileW;
+  const int tiles_y = (H3 + kMergeTileH - 1) / kMergeTileH;
+  const long long blocks = static_cast<long long>(tiles_x) * tiles_y * N;
+  if (blocks >= (1LL << 31)) return cudaErrorInvalidValue;
+  // the scales of upsample_add_t (align_corners = 0)
+  const float s54y = static_cast<float>(H5) / H4, s54x = static_cast<float>(W5) / W4;
+  const float s43y = static_cast<float>(H4) / H3, s43x = static_cast<float>(W4) / W3;
+  return launch_ex(merge_two_levels_kernel<T>, dim3(static_cast<unsigned>(blocks)), dim3(256),
+                   smem, s, opts, 1, static_cast<const T*>(m5), static_cast<const T*>(l4),
+                   static_cast<T*>(m4), static_cast<const T*>(l3), static_cast<T*>(m3), H5, W5,
+                   H4, W4, H3, W3, s54y, s54x, s43y, s43x, tiles_x, tiles_y, reg_h, reg_w, amax4,
+                   amax3, sc ? static_cast<T*>(sc->out) : nullptr, sc ? sc->scale_a : nullptr,
+                   sc ? sc->scale_w : nullptr);
+}
+}  // namespace
+
+cudaError_t launch_merge_two_levels(DType dt, const void* m5, const void* l4, void* m4,
+                                    const void* l3, void* m3, int N, int H5, int W5, int H4,
+                                    int W4, int H3, int W3, cudaStream_t s, unsigned* amax4,
+                                    unsigned* amax3, const MergeScaledCopy* m3_scaled,
+                                    LaunchOpts opts) {
+  if (dt != DType::BF16 && dt != DType::F16) return cudaErrorNotSupported;
+  if (N <= 0 || H5 <= 0 || W5 <= 0 || H4 <= 0 || W4 <= 0 || H3 <= 0 || W3 <= 0)
+    return cudaErrorInvalidValue;
+  if (H5 > H4 || W5 > W4 || H4 > H3 || W4 > W3) return cudaErrorNotSupported;  // upsampling
+  if (!m5 || !l4 || !m4 || !l3 || !m3) return cudaErrorInvalidValue;
+  if (l4 == m4) return cudaErrorInvalidValue;
+  if (!aligned16(m5) || !aligned16(l4) || !aligned16(m4) || !aligned16(l3) || !aligned16(m3))
+    return cudaErrorMisalignedAddress;
+  if (m3_scaled && (!m3_scaled->out || !m3_scaled->scale_a || !m3_scaled->scale_w ||
+                    !aligned16(m3_scaled->out)))
+    return cudaErrorInvalidValue;
+  return dt == DType::BF16
+             ? merge_two_levels_t<__nv_bfloat16>(m5, l4, m4, l3, m3, N, H5, W5, H4, W4, H3, W3,
+                                                 s, amax4, amax3, m3_scaled, opts)
+             : merge_two_levels_t<__half>(m5, l4, m4, l3, m3, N, H5, W5, H4, W4, H3, W3, s,
+                                          amax4, amax3, m3_scaled, opts);
 }
 
 cudaError_t launch_p6(DType dt, const void* in, void* out, int N, int C, int H, int W,
@@ -844,7 +1075,7 @@ cudaError_t launch_absmax(DType dt, const void* x, long long n, int groups, unsi
 
 cudaError_t launch_quantize_e4m3(DType dt, const void* x, long long n, int groups,
                                  const unsigned* amax_bits, void* q, float* scale_out,
-                                 cudaStream_t s, bool pdl) {
+                                 cudaStream_t s, LaunchOpts opts) {
   if (n <= 0 || !x || !q || !amax_bits) return cudaErrorInvalidValue;
   if (groups < 1 || groups > 65535 || n % groups != 0) return cudaErrorInvalidValue;
   const long long per = n / groups;
@@ -857,13 +1088,13 @@ cudaError_t launch_quantize_e4m3(DType dt, const void* x, long long n, int group
   uint8_t* qb = static_cast<uint8_t*>(q);
   switch (dt) {
     case DType::F32:
-      return launch_ex(quantize_e4m3_kernel<float>, g, dim3(256), 0, s, pdl, 1,
+      return launch_ex(quantize_e4m3_kernel<float>, g, dim3(256), 0, s, opts, 1,
                        static_cast<const float*>(x), n, vec, amax_bits, qb, scale_out);
     case DType::F16:
-      return launch_ex(quantize_e4m3_kernel<__half>, g, dim3(256), 0, s, pdl, 1,
+      return launch_ex(quantize_e4m3_kernel<__half>, g, dim3(256), 0, s, opts, 1,
                        static_cast<const __half*>(x), n, vec, amax_bits, qb, scale_out);
     case DType::BF16:
-      return launch_ex(quantize_e4m3_kernel<__nv_bfloat16>, g, dim3(256), 0, s, pdl, 1,
+      return launch_ex(quantize_e4m3_kernel<__nv_bfloat16>, g, dim3(256), 0, s, opts, 1,
                        static_cast<const __nv_bfloat16*>(x), n, vec, amax_bits, qb, scale_out);
     default:
       return cudaErrorInvalidValue;

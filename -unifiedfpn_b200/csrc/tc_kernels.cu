@@ -131,7 +131,7 @@ void fill_tiling(TcGemmArgs& a, int N, int H, int W, Conv3x3Tiling t) {
 }
 
 template <int kMode, typename T>
-cudaError_t launch_t(const TcPlan& p, cudaStream_t s, bool pdl) {
+cudaError_t launch_t(const TcPlan& p, cudaStream_t s, LaunchOpts opts) {
   static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -145,12 +145,12 @@ cudaError_t launch_t(const TcPlan& p, cudaStream_t s, bool pdl) {
   TcGemmArgs a;
   std::memcpy(&a, p.args, sizeof(a));
   return launch_ex(fpn_tc_gemm_kernel<kMode, T>, dim3(p.grid), dim3(TcCfgT<kMode, T>::kThreads),
-                   TcCfgT<kMode, T>::kSmemBytes, s, pdl, 1, p.map_a, p.map_b, p.map_out,
+                   TcCfgT<kMode, T>::kSmemBytes, s, opts, 1, p.map_a, p.map_b, p.map_out,
                    p.map_coarse, a);
 }
 
 template <typename T>
-cudaError_t launch_halo_t(const TcPlan& p, cudaStream_t s, bool pdl) {
+cudaError_t launch_halo_t(const TcPlan& p, cudaStream_t s, LaunchOpts opts) {
   static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -164,11 +164,11 @@ cudaError_t launch_halo_t(const TcPlan& p, cudaStream_t s, bool pdl) {
   TcGemmArgs a;
   std::memcpy(&a, p.args, sizeof(a));
   return launch_ex(fpn_conv3x3_halo_kernel<T>, dim3(p.grid), dim3(kTcThreads),
-                   HaloCfg::kSmemBytes, s, pdl, 1, p.map_a, p.map_b, p.map_out, a);
+                   HaloCfg::kSmemBytes, s, opts, 1, p.map_a, p.map_b, p.map_out, a);
 }
 
 template <typename T, bool kCvt = false>
-cudaError_t launch_halo_pair_t(const TcPlan& p, cudaStream_t s, bool pdl) {
+cudaError_t launch_halo_pair_t(const TcPlan& p, cudaStream_t s, LaunchOpts opts) {
   static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -182,7 +182,7 @@ cudaError_t launch_halo_pair_t(const TcPlan& p, cudaStream_t s, bool pdl) {
   TcGemmArgs a;
   std::memcpy(&a, p.args, sizeof(a));
   return launch_ex(fpn_conv3x3_halo_pair_kernel<T, kCvt>, dim3(p.grid),
-                   dim3(PairCfgT<kCvt>::kThreads), PairCfgT<kCvt>::kSmemBytes, s, pdl, 2,
+                   dim3(PairCfgT<kCvt>::kThreads), PairCfgT<kCvt>::kSmemBytes, s, opts, 2,
                    p.map_a, p.map_b, p.map_out, a);
 }
 
@@ -535,7 +535,7 @@ cudaError_t plan_neck(NeckPlan& plan, DType dt, int N, const NeckLevel* lv, void
 
 namespace {
 template <typename T>
-cudaError_t launch_neck_t(const NeckPlan& p, cudaStream_t s, bool pdl) {
+cudaError_t launch_neck_t(const NeckPlan& p, cudaStream_t s, LaunchOpts opts) {
   static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -547,40 +547,40 @@ cudaError_t launch_neck_t(const NeckPlan& p, cudaStream_t s, bool pdl) {
     configured[dev] = true;
   }
   const NeckParams* P = reinterpret_cast<const NeckParams*>(p.params);
-  return launch_ex(fpn_neck_kernel<T>, dim3(p.grid), dim3(kTcThreads), kNeckSmemBytes, s, pdl,
+  return launch_ex(fpn_neck_kernel<T>, dim3(p.grid), dim3(kTcThreads), kNeckSmemBytes, s, opts,
                    1, *P);
 }
 }  // namespace
 
-cudaError_t launch_neck(const NeckPlan& plan, cudaStream_t s, bool pdl) {
+cudaError_t launch_neck(const NeckPlan& plan, cudaStream_t s, LaunchOpts opts) {
   if (plan.grid <= 0) return cudaSuccess;
-  return plan.dtype == DType::BF16 ? launch_neck_t<__nv_bfloat16>(plan, s, pdl)
-                                   : launch_neck_t<__half>(plan, s, pdl);
+  return plan.dtype == DType::BF16 ? launch_neck_t<__nv_bfloat16>(plan, s, opts)
+                                   : launch_neck_t<__half>(plan, s, opts);
 }
 
-cudaError_t launch_tc(const TcPlan& plan, cudaStream_t s, bool pdl) {
+cudaError_t launch_tc(const TcPlan& plan, cudaStream_t s, LaunchOpts opts) {
   if (plan.grid <= 0) return cudaSuccess;
   if (plan.dtype == DType::E4M3) {
-    if (plan.mode == 0) return launch_t<0, __nv_fp8_e4m3>(plan, s, pdl);
-    if (plan.mode == 2) return launch_halo_t<__nv_fp8_e4m3>(plan, s, pdl);
-    if (plan.mode == 3) return launch_halo_pair_t<__nv_fp8_e4m3>(plan, s, pdl);
-    if (plan.mode == 4) return launch_halo_pair_t<__nv_fp8_e4m3, true>(plan, s, pdl);
+    if (plan.mode == 0) return launch_t<0, __nv_fp8_e4m3>(plan, s, opts);
+    if (plan.mode == 2) return launch_halo_t<__nv_fp8_e4m3>(plan, s, opts);
+    if (plan.mode == 3) return launch_halo_pair_t<__nv_fp8_e4m3>(plan, s, opts);
+    if (plan.mode == 4) return launch_halo_pair_t<__nv_fp8_e4m3, true>(plan, s, opts);
     return cudaErrorInvalidValue;
   }
   if (plan.mode == 3) {
-    return plan.dtype == DType::BF16 ? launch_halo_pair_t<__nv_bfloat16>(plan, s, pdl)
-                                     : launch_halo_pair_t<__half>(plan, s, pdl);
+    return plan.dtype == DType::BF16 ? launch_halo_pair_t<__nv_bfloat16>(plan, s, opts)
+                                     : launch_halo_pair_t<__half>(plan, s, opts);
   }
   if (plan.mode == 0) {
-    return plan.dtype == DType::BF16 ? launch_t<0, __nv_bfloat16>(plan, s, pdl)
-                                     : launch_t<0, __half>(plan, s, pdl);
+    return plan.dtype == DType::BF16 ? launch_t<0, __nv_bfloat16>(plan, s, opts)
+                                     : launch_t<0, __half>(plan, s, opts);
   }
   if (plan.mode == 2) {
-    return plan.dtype == DType::BF16 ? launch_halo_t<__nv_bfloat16>(plan, s, pdl)
-                                     : launch_halo_t<__half>(plan, s, pdl);
+    return plan.dtype == DType::BF16 ? launch_halo_t<__nv_bfloat16>(plan, s, opts)
+                                     : launch_halo_t<__half>(plan, s, opts);
   }
-  return plan.dtype == DType::BF16 ? launch_t<1, __nv_bfloat16>(plan, s, pdl)
-                                   : launch_t<1, __half>(plan, s, pdl);
+  return plan.dtype == DType::BF16 ? launch_t<1, __nv_bfloat16>(plan, s, opts)
+                                   : launch_t<1, __half>(plan, s, opts);
 }
 
 }  // namespace ufpn

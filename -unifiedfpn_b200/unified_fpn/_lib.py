@@ -56,7 +56,7 @@ SIGNATURES = {
     "ufpn_core_forward": (c_int, [c_void_p, POINTER(c_void_p), POINTER(c_void_p), c_void_p, c_void_p]),
     "ufpn_core_set_kernel_config": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int]),
     "ufpn_core_set_schedule": (c_int, [c_void_p, c_int]),
-    "ufpn_core_set_programmatic_launch": (c_int, [c_void_p, c_int]),
+    "ufpn_core_set_schedule_options": (c_int, [c_void_p, c_int, c_int, c_int]),
     "ufpn_core_trace_next_forward": (c_int, [c_void_p]),
     "ufpn_core_get_neck_trace": (c_int, [c_void_p, POINTER(ctypes.c_ulonglong)]),
     "ufpn_core_get_memory_usage": (c_size_t, [c_void_p]),
@@ -75,6 +75,9 @@ SIGNATURES = {
         c_int, [c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                 c_void_p]),
     "ufpn_p6_maxpool": (c_int, [c_int, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
+    "ufpn_merge_two_levels": (
+        c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
+                c_int, c_void_p]),
     "ufpn_pack_conv3x3_weights": (c_int, [c_int, c_void_p, c_void_p, c_int, c_int, c_void_p]),
     "ufpn_absmax": (c_int, [c_int, c_void_p, c_longlong, c_int, c_void_p, c_void_p]),
     "ufpn_quantize_e4m3": (c_int, [c_int, c_void_p, c_longlong, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),

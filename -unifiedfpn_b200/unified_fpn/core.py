@@ -285,17 +285,21 @@ class UnifiedFPN:
                                               _ACT[activation], int(enable_graph_capture)), "set_kernel_config")
 
     def set_schedule(self, fused_neck_kernel: bool = False, single_stream: bool = False,
-                     programmatic_launch: bool = True) -> None:
+                     programmatic_launch: bool = True, chain_priority: bool = False,
+                     merge_two_levels: bool = False) -> None:
         """Tensor-core schedule: one persistent kernel for the whole neck, or per-level
         kernels on several streams (default) or, with ``single_stream``, one after the other
         on the caller's stream (bitwise the same results as the default).
         ``programmatic_launch`` (16-bit split schedule): kernels that follow a kernel on the
         main stream start during its tail and wait on the device for its results (same
-        results, less launch latency)."""
+        results, less launch latency).  ``chain_priority`` (16-bit split schedule): the
+        main-stream chain gets the device's highest launch priority.  ``merge_two_levels``:
+        the P4 and P3 top-down merges in one launch (when the maps upsample; set it before
+        the first forward of a geometry)."""
         mode = 1 if fused_neck_kernel else (2 if single_stream else 0)
         check(lib.ufpn_core_set_schedule(self._h, mode), "set_schedule")
-        check(lib.ufpn_core_set_programmatic_launch(self._h, int(programmatic_launch)),
-              "set_programmatic_launch")
+        check(lib.ufpn_core_set_schedule_options(self._h, int(programmatic_launch), int(chain_priority),
+                                                 int(merge_two_levels)), "set_schedule_options")
 
     def neck_timeline(self, backbone_features) -> dict:
         """Runs one forward with the fused neck kernel's device timeline recorded and

@@ -154,6 +154,28 @@ def fpn_upsample_add(coarse: torch.Tensor, lateral: torch.Tensor | None = None,
     return out
 
 
+def fpn_merge_two_levels(m5: torch.Tensor, l4: torch.Tensor, l3: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Two top-down steps in one launch: ``M4 = l4 + up(m5)``, ``M3 = l3 + up(M4)``
+    (channels-last, 256 channels, bf16 / fp16, each map upsampling to the next).  Returns
+    (M4, M3); bitwise the same as two ``fpn_upsample_add`` calls.  Reference: two iterations
+    of the top-down loop, lib/core/fpn_engine.cu:230-245 with launch_upsample_and_add
+    (:274-313)."""
+    _check_cuda(m5, l4, l3)
+    dt = dtype_code(m5)
+    for t in (m5, l4, l3):
+        if t.dtype != m5.dtype or t.shape[1] != 256 or t.shape[0] != m5.shape[0]:
+            raise ValueError("m5, l4, l3 must share dtype and batch and have 256 channels")
+    cl = torch.channels_last
+    m5, l4 = m5.contiguous(memory_format=cl), l4.contiguous(memory_format=cl)
+    m3 = l3.contiguous(memory_format=cl).clone(memory_format=cl)
+    m4 = torch.empty_like(l4, memory_format=cl)
+    N = m5.shape[0]
+    check(lib.ufpn_merge_two_levels(dt, m5.data_ptr(), l4.data_ptr(), m4.data_ptr(), m3.data_ptr(), N,
+                                    m5.shape[2], m5.shape[3], l4.shape[2], l4.shape[3], l3.shape[2],
+                                    l3.shape[3], _stream(m5)), "ufpn_merge_two_levels")
+    return m4, m3
+
+
 def fpn_upsample_bilinear(input: torch.Tensor, scale_factor: float) -> torch.Tensor:
     """Bilinear upsample by ``scale_factor``; output size = int(in * scale), sampled
     with scale = in / out (half-pixel, align_corners=False).

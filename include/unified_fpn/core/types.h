@@ -148,6 +148,17 @@ struct FPNKernelConfig {
   // tail, sets up and waits on the device for the predecessor's results), hiding launch
   // latency and prologues along the P5 -> P2 chain.  (Not used by the e4m3 schedule.)
   bool programmatic_launch = true;
+  // 16-bit split schedule: launch the main-stream chain (laterals, merges, P2 3x3) at the
+  // device's highest launch priority, the side streams' 3x3s at the default one.  Off:
+  // measured 1.4% slower at the R50 800x1216 batch-2 workload (the chain's CTAs then take
+  // every freed SM and the side 3x3s pile up behind the P2 3x3).
+  bool chain_priority = false;
+  // Tensor-core split schedules: merge M4 and M3 in one launch when the maps upsample
+  // (merge_two_levels; set before the first forward of a geometry, which allocates its raw-L4
+  // buffer), else per level in place.  Off: measured slower end to end at the R50 800x1216
+  // batch-2 and 640x640 batch-16 workloads (one launch, but the P4 3x3 then waits for both
+  // merges and the tiles form a single wave that other streams' CTAs cut short).
+  bool merge_two_levels = false;
 };
 
 struct FPNWeights {

@@ -31,6 +31,18 @@ inline int dtype_size(DType d) {
 }
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Launch options of the launchers that take them.
+//   pdl: programmatic dependent launch -- the kernel may be scheduled while the previous
+//        kernel of stream s still runs; it sets up, then waits for that kernel's completion
+//        before touching memory (griddepcontrol.wait).  Only for a launch whose predecessor
+//        in the stream is a kernel.
+//   priority: launch priority (cudaLaunchAttributePriority; lower = dispatched first when
+//        CTAs of several kernels wait for SMs); 0 keeps the stream's.
+struct LaunchOpts {
+  bool pdl = false;
+  int priority = 0;
+};
+
 // ---- bandwidth kernels (simt_kernels.cu)
 // A second, per-channel scaled copy of an upsample-add result: out[c] / (scale_a[0] *
 // scale_w[c]), same layout (NHWC, 256 channels of a 16-bit type only).
@@ -44,7 +56,19 @@ struct MergeScaledCopy {
 cudaError_t launch_upsample_add(DType dt, const void* coarse, const void* lat, void* out, int N,
                                 int C, int Hc, int Wc, int H, int W, int align_corners,
                                 Layout layout, cudaStream_t s, unsigned* amax_out = nullptr,
-                                const MergeScaledCopy* scaled = nullptr, bool pdl = false);
+                                const MergeScaledCopy* scaled = nullptr,
+                                LaunchOpts opts = LaunchOpts());
+// Two top-down merges in one launch (NHWC, 256 channels, bf16 / fp16, maps that upsample):
+// M4 = L4 + up(M5) into m4 and M3 = L3 + up(M4) in place (l3 may alias m3; l4 must not
+// alias m4).  Bitwise the same as launch_upsample_add for M4 then for M3 (the reference's
+// top-down loop, fpn_engine.cu:274-313, two iterations).  amax4 / amax3 / m3_scaled: as
+// amax_out / scaled of launch_upsample_add, for M4, M3 and M3.
+cudaError_t launch_merge_two_levels(DType dt, const void* m5, const void* l4, void* m4,
+                                    const void* l3, void* m3, int N, int H5, int W5, int H4,
+                                    int W4, int H3, int W3, cudaStream_t s,
+                                    unsigned* amax4 = nullptr, unsigned* amax3 = nullptr,
+                                    const MergeScaledCopy* m3_scaled = nullptr,
+                                    LaunchOpts opts = LaunchOpts());
 // ---- e4m3 quantisation (simt_kernels.cu).  scale = amax / 448, q = e4m3_rn_satfinite(
 // x * (448 / amax)) (amax == 0: scale = 1, q = 0); amax carried as fp32 bits.
 // The n elements form `groups` equal consecutive groups (images), each with its own
@@ -56,7 +80,7 @@ cudaError_t launch_absmax(DType dt, const void* x, long long n, int groups, unsi
 // scales to scale_out[groups] (device, may be null).
 cudaError_t launch_quantize_e4m3(DType dt, const void* x, long long n, int groups,
                                  const unsigned* amax_bits, void* q, float* scale_out,
-                                 cudaStream_t s, bool pdl = false);
+                                 cudaStream_t s, LaunchOpts opts = LaunchOpts());
 // Per-row (output channel) quantisation of fp32 weights [rows][cols] -> e4m3 + scales[rows].
 // pack_cin > 0: rows are [pack_cin][3][3] and q is written [9][pack_cin] (3x3 K order).
 cudaError_t launch_quantize_rows_e4m3(const float* w, int rows, int cols, int pack_cin, void* q,
@@ -206,12 +230,8 @@ struct NeckJobSpec {
 cudaError_t plan_neck_jobs(NeckPlan& plan, DType dt, int N, const NeckLevel* levels, void* p6,
                            const NeckJobSpec* specs, int num_specs, int* sched, int* status,
                            int max_ctas, unsigned long long* trace = nullptr);
-// pdl (every launcher that takes it): programmatic dependent launch -- the kernel may be
-// scheduled while the previous kernel of stream s still runs; it sets up, then waits for
-// that kernel's completion before touching memory (griddepcontrol.wait).  Only for a launch
-// whose predecessor in the stream is a kernel.
-cudaError_t launch_neck(const NeckPlan& plan, cudaStream_t s, bool pdl = false);
-cudaError_t launch_tc(const TcPlan& plan, cudaStream_t s, bool pdl = false);
+cudaError_t launch_neck(const NeckPlan& plan, cudaStream_t s, LaunchOpts opts = LaunchOpts());
+cudaError_t launch_tc(const TcPlan& plan, cudaStream_t s, LaunchOpts opts = LaunchOpts());
 
 // Number of SMs on the current device (cached).
 int sm_count();

@@ -82,10 +82,16 @@ int ufpn_core_set_kernel_config(ufpn_core* core, int tile_size, int channels_per
  * No reference counterpart (its engine launched 16 kernels on four unordered streams,
  * fpn_engine.cu:191-245). */
 int ufpn_core_set_schedule(ufpn_core* core, int fused_neck_kernel);
-/* 16-bit split schedule: 1 (default) = kernels that follow a kernel on the main stream are
+/* Split-schedule options (results are the same either way), 16-bit inputs:
+ * programmatic_launch 1 (default) = kernels that follow a kernel on the main stream are
  * programmatic dependent launches (scheduled during the predecessor's tail, waiting on the
- * device for its results); 0 = ordinary stream order.  Results are the same either way. */
-int ufpn_core_set_programmatic_launch(ufpn_core* core, int enable);
+ * device for its results), 0 = ordinary stream order; chain_priority 1 = the main-stream
+ * chain runs at the device's highest launch priority, 0 (default) = default priority;
+ * every tensor-core input type: merge_two_levels 1 = the P4 and P3 top-down merges in one
+ * launch when the maps upsample (set before the first forward of a geometry), 0 (default)
+ * = one in-place merge per level. */
+int ufpn_core_set_schedule_options(ufpn_core* core, int programmatic_launch, int chain_priority,
+                                   int merge_two_levels);
 /* fpn_engine.cu:408-415 (get_memory_usage) */
 size_t ufpn_core_get_memory_usage(const ufpn_core* core);
 /* fpn_pytorch.cpp:171-187 (get_performance_breakdown): kernel_times_ms[8], metrics[5] =
@@ -138,6 +144,14 @@ int ufpn_conv3x3(int dtype, const void* x, const void* w, const float* bias, voi
 int ufpn_upsample_add(int dtype, int layout, const void* coarse, const void* lateral, void* out,
                       int N, int C, int Hc, int Wc, int H, int W, int align_corners,
                       void* stream);
+
+/* Two iterations of the top-down loop in one launch (NHWC, 256 channels, bf16 / fp16, maps
+ * that upsample): m4 = l4 + bilinear(m5), then m3 = l3 + bilinear(m4), written in place over
+ * l3.  Bitwise equal to two ufpn_upsample_add calls.  l4 must not alias m4.  Replaces two
+ * iterations of the loop of UnifiedFPNCore::forward (fpn_engine.cu:230-245) calling
+ * launch_upsample_and_add (fpn_engine.cu:274-313). */
+int ufpn_merge_two_levels(int dtype, const void* m5, const void* l4, void* m4, void* l3_m3, int N,
+                          int H5, int W5, int H4, int W4, int H3, int W3, void* stream);
 
 /* P6 = max_pool2d(P5, kernel 1, stride 2).  No reference counterpart (the reference never
  * produces P6 although it takes C6, python/fpn_pytorch.cpp:84-86). */

@@ -72,6 +72,31 @@ def test_upsample_add(cuda_device, dtype, layout, sizes):
         assert y.is_contiguous(memory_format=torch.channels_last)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("geom", [
+    (2, (25, 38), (50, 76), (100, 152)),   # R50 800x1216 P5 / P4 / P3
+    (3, (42, 25), (84, 50), (167, 100)),   # 1333x800 (odd sizes, ratio not exactly 2)
+    (1, (5, 7), (9, 13), (17, 26)),        # small, ragged tiles on both edges
+    (2, (20, 20), (20, 20), (40, 40)),     # equal-size step (scale 1) then x2
+])
+def test_merge_two_levels_bitwise_equals_two_merges(cuda_device, dtype, geom):
+    import unified_fpn as U
+    n, (h5, w5), (h4, w4), (h3, w3) = geom
+    g = torch.Generator().manual_seed(11)
+    m5, l4, l3 = (_cl(torch.randn(n, 256, h, w, generator=g).to(dtype).to(cuda_device))
+                  for h, w in ((h5, w5), (h4, w4), (h3, w3)))
+    m4, m3 = U.fpn_merge_two_levels(m5, l4, l3)
+    m4_ref = U.fpn_upsample_add(m5, l4)
+    m3_ref = U.fpn_upsample_add(m4_ref, l3)
+    assert torch.equal(m4, m4_ref)
+    assert torch.equal(m3, m3_ref)
+    # and against the oracle's two top-down steps
+    r4 = l4.cpu().float() + O.bilinear_upsample_t(m5.cpu().float(), (h4, w4))
+    r3 = l3.cpu().float() + O.bilinear_upsample_t(r4.to(dtype).float(), (h3, w3))
+    assert O.rel_err(m4.cpu(), r4) < BF16_TOL
+    assert O.rel_err(m3.cpu(), r3) < BF16_TOL
+
+
 def test_reference_abi_upsample_half_and_bf16(cuda_device):
     from unified_fpn import _lib
     x = torch.randn(2, 64, 13, 19)

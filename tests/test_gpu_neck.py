@@ -147,6 +147,7 @@ def test_profiled_forward_breakdown(cuda_device):
     base = _run(fpn, feats)
     kt, mt = fpn.get_performance_breakdown(feats)
     assert (kt > 0).all()
+    # grouped P5/P4/P3 laterals, P4 and P3 merges, P2 lateral, 4 x 3x3
     assert mt[0] > 0 and mt[4] == 8
     prof = _run(fpn, feats)  # profiling is one-shot; results must match
     for a, b in zip(base, prof):
@@ -231,3 +232,27 @@ def test_single_stream_schedule_is_bitwise_equal(cuda_device, fp8):
     assert fpn.device_status() == 0
     for a, b in zip(two, one):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("fp8", [False, True])
+def test_schedule_options_are_bitwise_equal(cuda_device, fp8):
+    """Programmatic launches, chain priority and the one-launch P4 + P3 merge change only
+    when kernels run, not what they compute."""
+    import unified_fpn as U
+    chans, sizes = O.R50_CHANNELS, O.level_sizes(160, 224)
+    fs = [_cl(f.cuda()) for f in O.make_features(2, chans, sizes, seed=62, dist="normal")]
+    if fp8:
+        qs = [U.quantize_fp8(f) for f in fs]
+        feats, sc = [q for q, _ in qs], torch.cat([s for _, s in qs])
+    else:
+        feats, sc = [f.to(torch.bfloat16) for f in fs], None
+    ref = _run(U.UnifiedFPN(), feats, input_scales=sc)
+    for pl, pr, m2 in [(False, False, False), (True, False, True), (False, True, True)]:
+        fpn = U.UnifiedFPN()
+        fpn.set_schedule(programmatic_launch=pl, chain_priority=pr, merge_two_levels=m2)
+        outs = _run(fpn, feats, input_scales=sc)
+        assert fpn.device_status() == 0
+        for a, b in zip(ref, outs):
+            assert torch.equal(a, b), (pl, pr, m2)
+        if m2 and not fp8:
+            assert int(fpn.get_performance_breakdown(feats, input_scales=sc)[1][4].item()) == 7
