@@ -329,6 +329,33 @@ int ufpn_lateral_conv(int dtype, int layout, const void* x, const void* w, const
   return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "lateral launch");
 }
 
+int ufpn_lateral_conv_pair(int dtype, const void* x, const void* w, const float* bias,
+                           const void* coarse, void* out, int N, int Cin, int H, int W, int Hc,
+                           int Wc, void* stream) {
+  DType dt;
+  if (!parse_dtype(dtype, &dt)) return fail(UFPN_ERR_UNSUPPORTED, "unsupported dtype");
+  if (dt != DType::BF16 && dt != DType::F16)
+    return fail(UFPN_ERR_UNSUPPORTED, "the CTA-pair lateral takes bf16 or fp16");
+  if (!x || !w || !bias || !out) return fail(UFPN_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (N <= 0 || Cin <= 0 || H <= 0 || W <= 0)
+    return fail(UFPN_ERR_INVALID_ARG, "sizes must be positive");
+  if (coarse && (Hc <= 0 || Wc <= 0 || Hc > H || Wc > W))
+    return fail(UFPN_ERR_INVALID_ARG, "coarse map must be non-empty and not larger than output");
+  if (Cin % 8 != 0) return fail(UFPN_ERR_UNSUPPORTED, "Cin must be a multiple of 8");
+  if (!ufpn::aligned16(x) || !ufpn::aligned16(w) || !ufpn::aligned16(out) ||
+      !ufpn::aligned16(bias) || (coarse && !ufpn::aligned16(coarse)))
+    return fail(UFPN_ERR_ALIGNMENT, "tensors must be 16-byte aligned");
+  ufpn::TcPlan plan;
+  cudaError_t e = ufpn::plan_tc_lateral_pair(plan, dt, x, w, bias, coarse, out, N, Cin, H, W,
+                                             coarse ? Hc : 0, coarse ? Wc : 0,
+                                             ufpn::default_tiling(H, W), device_status_word(), 0);
+  if (e == cudaErrorNotSupported)
+    return fail(UFPN_ERR_UNSUPPORTED, "CTA-pair lateral: needs Cin <= 256 and a 64-pixel tap box");
+  if (e != cudaSuccess) return cuda_fail(e, "plan lateral pair");
+  e = ufpn::launch_tc(plan, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "lateral pair launch");
+}
+
 int ufpn_conv3x3(int dtype, const void* x, const void* w, const float* bias, void* out, void* p6,
                  int N, int H, int W, int tile_w, void* stream) {
   DType dt;

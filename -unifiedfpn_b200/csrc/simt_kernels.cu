@@ -82,6 +82,39 @@ struct Vec16 {
   };
 };
 
+// Two 16-bit values in one 32-bit word <-> two floats, with one packed round-to-nearest
+// conversion per pair (the same rounding as two scalar conversions).
+template <typename T>
+struct Pair16;
+template <>
+struct Pair16<__nv_bfloat16> {
+  __device__ static __forceinline__ float2 unpack(uint32_t w) {
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+  }
+  __device__ static __forceinline__ uint32_t pack(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  // fp32 bits of the larger of two 16-bit magnitudes packed in m (|x| bits, order-preserving)
+  __device__ static __forceinline__ uint32_t mag_to_f32_bits(uint32_t m) {
+    return max(m & 0xFFFFu, m >> 16) << 16;
+  }
+};
+template <>
+struct Pair16<__half> {
+  __device__ static __forceinline__ float2 unpack(uint32_t w) {
+    return __half22float2(*reinterpret_cast<const __half2*>(&w));
+  }
+  __device__ static __forceinline__ uint32_t pack(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __device__ static __forceinline__ uint32_t mag_to_f32_bits(uint32_t m) {
+    const unsigned short mx = static_cast<unsigned short>(max(m & 0xFFFFu, m >> 16));
+    return __float_as_uint(__half2float(__ushort_as_half(mx)));
+  }
+};
+
 // |v| as fp32 bits (orders like an unsigned integer).
 __device__ __forceinline__ uint32_t abs_bits(float v) { return __float_as_uint(v) & 0x7FFFFFFFu; }
 
@@ -198,15 +231,19 @@ __global__ void __launch_bounds__(256) upsample_add_nhwc_kernel(
   }
 }
 
-// Fast path for 512-byte pixels (256 channels of a 16-bit type -- every FPN map): one
-// warp per output pixel, lane = 16 bytes (8 channels), a block = 8 consecutive pixels of
-// one row, no loops; all five loads of a lane are independent and issued back to back.
-// `out` may alias `lat` (each lane reads its lateral vector before writing it).
+// Fast path for 512-byte pixels (256 channels of a 16-bit type -- every FPN map).  A unit is
+// 8 consecutive pixels of one output row, one per warp, lane = 16 bytes (8 channels).  A
+// block takes a contiguous run of units and walks it kU units at a time, issuing the five
+// 16-byte loads of every unit of the batch (lateral + 4 coarse corners) before any math, so
+// each thread keeps 5 * kU independent loads in flight; the grid is sized to the blocks that
+// are resident at once.  `out` may alias `lat`: each lane reads a lateral vector before it
+// writes that vector, and the pixels of a batch are distinct.
 // amax (optional): amax[n] = atomicMax of |out| of image n as fp32 bits (for a following
-// per-image e4m3 quantisation).  out_s (optional): a second copy of out with channel c
-// multiplied by 1 / (scale_a[0] * scale_w[c]) (the e4m3 P2 lateral adds this copy through
-// its tensor-core top-down k-block before it scales its accumulator by the same factor).
-template <typename T>
+// per-image e4m3 quantisation), one block-reduced publication per image a run touches.
+// out_s (optional): a second copy of out with channel c multiplied by
+// 1 / (scale_a[0] * scale_w[c]) (the e4m3 P2 lateral adds this copy through its tensor-core
+// top-down k-block before it scales its accumulator by the same factor).
+template <typename T, int kU>
 __global__ void __launch_bounds__(256) upsample_add_px512_kernel(
     const T* __restrict__ coarse, const T* lat, T* out, int N, int Hc, int Wc, int H, int W,
     int chunks, float sy_scale, float sx_scale, int ac, unsigned* amax, T* out_s,
@@ -224,61 +261,99 @@ __global__ void __launch_bounds__(256) upsample_add_px512_kernel(
   }
   unsigned m = 0;
   int m_img = -1;  // image the running maximum m belongs to (block-uniform)
-  // units_per_block == 0: one unit per block, strided (most loads in flight);
-  // > 0: a contiguous run of units per block, so a block crosses few image boundaries
-  // (one absmax publication per image it touches).
   const long long total = static_cast<long long>(N) * H * chunks;
-  const long long u0 = units_per_block ? blockIdx.x * static_cast<long long>(units_per_block)
-                                       : blockIdx.x;
-  const long long u1 = units_per_block ? min(total, u0 + units_per_block) : total;
-  const long long du = units_per_block ? 1 : gridDim.x;
-  for (long long u = u0; u < u1; u += du) {
-    const int r = static_cast<int>(u / chunks);
-    const int n = r / H;
-    if (amax && n != m_img) {
-      if (m_img >= 0) publish_amax_block(amax + m_img, m, red);
-      m = 0;
-      m_img = n;
-    }
-    const int x = static_cast<int>(u - static_cast<long long>(r) * chunks) * 8 + warp;
-    if (x >= W) continue;
-    const int y = r - n * H;
-    const float sy = src_coord(y, Hc, H, sy_scale, ac);
-    const float sx = src_coord(x, Wc, W, sx_scale, ac);
-    const int y0 = static_cast<int>(sy), x0 = static_cast<int>(sx);
-    const int y1 = min(y0 + 1, Hc - 1), x1 = min(x0 + 1, Wc - 1);
-    const float wy = sy - static_cast<float>(y0), wx = sx - static_cast<float>(x0);
-    const size_t io = (static_cast<size_t>(r) * W + x) * 256 + lane * 8;
-    const T* cb = coarse + static_cast<size_t>(n) * Hc * Wc * 256 + lane * 8;
-    Vec16<T> l, a, b, c, d;
-    if (lat) l.u = *reinterpret_cast<const uint4*>(lat + io);
-    a.u = __ldg(reinterpret_cast<const uint4*>(cb + (static_cast<size_t>(y0) * Wc + x0) * 256));
-    b.u = __ldg(reinterpret_cast<const uint4*>(cb + (static_cast<size_t>(y0) * Wc + x1) * 256));
-    c.u = __ldg(reinterpret_cast<const uint4*>(cb + (static_cast<size_t>(y1) * Wc + x0) * 256));
-    d.u = __ldg(reinterpret_cast<const uint4*>(cb + (static_cast<size_t>(y1) * Wc + x1) * 256));
-    const float w00 = (1.f - wy) * (1.f - wx), w01 = (1.f - wy) * wx;
-    const float w10 = wy * (1.f - wx), w11 = wy * wx;
-    Vec16<T> o;
+  const long long u0 = static_cast<long long>(blockIdx.x) * units_per_block;
+  const long long u1 = min(total, u0 + units_per_block);
+  // position of the run's first unit (the only divisions); later units step from it
+  int r = static_cast<int>(u0 / chunks);  // output row over all images
+  int ci = static_cast<int>(u0 - static_cast<long long>(r) * chunks);
+  int n = r / H;
+  int y = r - n * H;
+  for (long long ub = u0; ub < u1; ub += kU) {
+    Vec16<T> l[kU], a[kU], b[kU], c[kU], d[kU];
+    float wy[kU], wx[kU];
+    size_t io[kU];
+    int img[kU];
+    bool live[kU];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      float v = lat ? to_f(l.e[e]) : 0.f;
-      v = fmaf(to_f(a.e[e]), w00, v);
-      v = fmaf(to_f(b.e[e]), w01, v);
-      v = fmaf(to_f(c.e[e]), w10, v);
-      v = fmaf(to_f(d.e[e]), w11, v);
-      o.e[e] = from_f<T>(v);
-      m = max(m, abs_bits(to_f(o.e[e])));
+    for (int k = 0; k < kU; ++k) {
+      const bool in_run = ub + k < u1;
+      const int x = ci * 8 + warp;
+      live[k] = in_run && x < W;
+      img[k] = n;
+      const int xc = min(x, W - 1);
+      const int rk = r, yk = y, nk = n;
+      if (++ci == chunks) {  // step to the next unit
+        ci = 0;
+        ++r;
+        if (++y == H) {
+          y = 0;
+          ++n;
+        }
+      }
+      if (!in_run) continue;  // past the run: nothing loaded, nothing stored
+      const float sy = src_coord(yk, Hc, H, sy_scale, ac);
+      const float sx = src_coord(xc, Wc, W, sx_scale, ac);
+      const int y0 = static_cast<int>(sy), x0 = static_cast<int>(sx);
+      const int y1 = min(y0 + 1, Hc - 1), x1 = min(x0 + 1, Wc - 1);
+      wy[k] = sy - static_cast<float>(y0);
+      wx[k] = sx - static_cast<float>(x0);
+      io[k] = (static_cast<size_t>(rk) * W + xc) * 256 + lane * 8;
+      const T* cb = coarse + static_cast<size_t>(nk) * Hc * Wc * 256 + lane * 8;
+      if (lat) l[k].u = *reinterpret_cast<const uint4*>(lat + io[k]);
+      a[k].u = __ldg(reinterpret_cast<const uint4*>(cb + (static_cast<size_t>(y0) * Wc + x0) * 256));
+      b[k].u = __ldg(reinterpret_cast<const uint4*>(cb + (static_cast<size_t>(y0) * Wc + x1) * 256));
+      c[k].u = __ldg(reinterpret_cast<const uint4*>(cb + (static_cast<size_t>(y1) * Wc + x0) * 256));
+      d[k].u = __ldg(reinterpret_cast<const uint4*>(cb + (static_cast<size_t>(y1) * Wc + x1) * 256));
     }
-    *reinterpret_cast<uint4*>(out + io) = o.u;
-    if (out_s) {
-      Vec16<T> os;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) os.e[e] = from_f<T>(to_f(o.e[e]) * inv[e]);
-      *reinterpret_cast<uint4*>(out_s + io) = os.u;
+    for (int k = 0; k < kU; ++k) {
+      if (ub + k >= u1) break;  // block-uniform
+      if (amax && img[k] != m_img) {  // block-uniform: the image of a unit
+        if (m_img >= 0) publish_amax_block(amax + m_img, m, red);
+        m = 0;
+        m_img = img[k];
+      }
+      if (!live[k]) continue;
+      const float w00 = (1.f - wy[k]) * (1.f - wx[k]), w01 = (1.f - wy[k]) * wx[k];
+      const float w10 = wy[k] * (1.f - wx[k]), w11 = wy[k] * wx[k];
+      const uint32_t lw[4] = {l[k].u.x, l[k].u.y, l[k].u.z, l[k].u.w};
+      const uint32_t aw[4] = {a[k].u.x, a[k].u.y, a[k].u.z, a[k].u.w};
+      const uint32_t bw[4] = {b[k].u.x, b[k].u.y, b[k].u.z, b[k].u.w};
+      const uint32_t cw[4] = {c[k].u.x, c[k].u.y, c[k].u.z, c[k].u.w};
+      const uint32_t dw[4] = {d[k].u.x, d[k].u.y, d[k].u.z, d[k].u.w};
+      uint32_t ow[4], mag = 0;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {  // channel pairs: same fp32 chain per channel as ever
+        const float2 fl = lat ? Pair16<T>::unpack(lw[e]) : make_float2(0.f, 0.f);
+        const float2 fa = Pair16<T>::unpack(aw[e]), fb = Pair16<T>::unpack(bw[e]);
+        const float2 fc = Pair16<T>::unpack(cw[e]), fd = Pair16<T>::unpack(dw[e]);
+        float v0 = fmaf(fa.x, w00, fl.x), v1 = fmaf(fa.y, w00, fl.y);
+        v0 = fmaf(fb.x, w01, v0);
+        v1 = fmaf(fb.y, w01, v1);
+        v0 = fmaf(fc.x, w10, v0);
+        v1 = fmaf(fc.y, w10, v1);
+        v0 = fmaf(fd.x, w11, v0);
+        v1 = fmaf(fd.y, w11, v1);
+        ow[e] = Pair16<T>::pack(v0, v1);
+        mag = __vmaxu2(mag, ow[e] & 0x7FFF7FFFu);
+      }
+      if (amax) m = max(m, Pair16<T>::mag_to_f32_bits(mag));
+      *reinterpret_cast<uint4*>(out + io[k]) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+      if (out_s) {
+        uint32_t sw[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = Pair16<T>::unpack(ow[e]);
+          sw[e] = Pair16<T>::pack(f.x * inv[2 * e], f.y * inv[2 * e + 1]);
+        }
+        *reinterpret_cast<uint4*>(out_s + io[k]) = make_uint4(sw[0], sw[1], sw[2], sw[3]);
+      }
     }
   }
   if (amax && m_img >= 0) publish_amax_block(amax + m_img, m, red);
 }
+constexpr int kPx512Batch = 4;
 
 // ---------------------------------------------------------------- two-level merge
 // M4 = L4 + up(M5) and M3 = L3 + up(M4) in ONE launch (NHWC, 256 channels of a 16-bit type,
@@ -832,22 +907,29 @@ cudaError_t upsample_add_t(const void* coarse, const void* lat, void* out, int N
     if constexpr (sizeof(T) == 2) {
       if (vec && C == 256) {
         const int chunks = (W + 7) / 8;
-        const long long blocks = static_cast<long long>(N) * H * chunks;
-        int grid = blocks < (1LL << 30) ? static_cast<int>(blocks) : (1 << 30);
-        int per = 0;
-        if (amax) {
-          // With an absmax: contiguous runs of units per block (8 resident 256-thread blocks
-          // per SM), so a block crosses few image boundaries and publishes a handful of
-          // block-reduced maxima.  (One unit per block with a block reduction each measured
-          // 1.5x slower: 12800 reductions at the 640x640 batch-16 P3 map.)
-          const long long g = blocks < 148LL * 8 ? blocks : 148LL * 8;
-          per = static_cast<int>((blocks + g - 1) / g);
-          grid = static_cast<int>((blocks + per - 1) / per);
+        const long long units = static_cast<long long>(N) * H * chunks;
+        auto kern = upsample_add_px512_kernel<T, kPx512Batch>;
+        // grid = the blocks resident at once, each with a contiguous run of units
+        static int resident[64] = {};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (dev < 64 && resident[dev] == 0) {
+          int per_sm = 0;
+          cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, 0);
+          if (e != cudaSuccess) return e;
+          int sms = 0;
+          cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+          resident[dev] = (per_sm > 0 ? per_sm : 1) * (sms > 0 ? sms : 148);
         }
-        return launch_ex(upsample_add_px512_kernel<T>, dim3(grid), dim3(256), 0, s, opts, 1, c, l,
-                         o, N, Hc, Wc, H, W, chunks, sy, sx, ac, amax,
-                         sc ? static_cast<T*>(sc->out) : nullptr, sc ? sc->scale_a : nullptr,
-                         sc ? sc->scale_w : nullptr, per);
+        const long long g = units < resident[dev < 64 ? dev : 0] ? units : resident[dev < 64 ? dev : 0];
+        if (g <= 0) return cudaSuccess;
+        const long long per = (units + g - 1) / g;
+        if (per >= (1LL << 31)) return cudaErrorInvalidValue;
+        const int grid = static_cast<int>((units + per - 1) / per);
+        return launch_ex(kern, dim3(grid), dim3(256), 0, s, opts, 1, c, l, o, N, Hc, Wc, H, W,
+                         chunks, sy, sx, ac, amax, sc ? static_cast<T*>(sc->out) : nullptr,
+                         sc ? sc->scale_a : nullptr, sc ? sc->scale_w : nullptr,
+                         static_cast<int>(per));
       }
     }
     if (sc) return cudaErrorNotSupported;  // the scaled copy exists on the 256-channel path

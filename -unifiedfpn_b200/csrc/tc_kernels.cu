@@ -8,6 +8,7 @@
 
 #include "conv_pair.cuh"
 #include "kernels.h"
+#include "lateral_pair.cuh"
 #include "neck_kernel.cuh"
 #include "tc_gemm.cuh"
 
@@ -186,6 +187,24 @@ cudaError_t launch_halo_pair_t(const TcPlan& p, cudaStream_t s, LaunchOpts opts)
                    p.map_a, p.map_b, p.map_out, a);
 }
 
+template <typename T>
+cudaError_t launch_lateral_pair_t(const TcPlan& p, cudaStream_t s, LaunchOpts opts) {
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(fpn_lateral_pair_kernel<T>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         LpCfg::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  TcGemmArgs a;
+  std::memcpy(&a, p.args, sizeof(a));
+  return launch_ex(fpn_lateral_pair_kernel<T>, dim3(p.grid), dim3(kTcThreads), LpCfg::kSmemBytes,
+                   s, opts, 2, p.map_a, p.map_b, p.map_out, p.map_coarse, a);
+}
+
 }  // namespace
 
 int sm_count() {
@@ -286,6 +305,27 @@ cudaError_t plan_tc_lateral(TcPlan& plan, DType dt, const void* x, const void* w
   plan.num_tiles = a.num_tiles;
   const int cap = max_ctas > 0 ? max_ctas : sm_count();
   plan.grid = a.num_tiles < cap ? a.num_tiles : cap;
+  return cudaSuccess;
+}
+
+cudaError_t plan_tc_lateral_pair(TcPlan& plan, DType dt, const void* x, const void* w,
+                                 const float* bias, const void* coarse, void* out, int N,
+                                 int Cin, int H, int W, int Hc, int Wc, Conv3x3Tiling tiling,
+                                 int* status, int max_ctas) {
+  if (dt != DType::BF16 && dt != DType::F16) return cudaErrorNotSupported;
+  cudaError_t e = plan_tc_lateral(plan, dt, x, w, bias, coarse, out, N, Cin, H, W, Hc, Wc, tiling,
+                                  status, max_ctas);
+  if (e != cudaSuccess) return e;
+  TcGemmArgs a;
+  std::memcpy(&a, plan.args, sizeof(a));
+  // resident weight halves must fit; a top-down add needs its staged coarse box
+  if (a.num_kb > kLpMaxKb || (coarse && a.cbox_w <= 0)) return cudaErrorNotSupported;
+  if ((e = encode_weights(&plan.map_b, dt, w, Cin, kTcBlockN / 2)) != cudaSuccess) return e;
+  plan.mode = 5;
+  const int units = (a.num_tiles + 1) / 2;
+  const int cap = (max_ctas > 0 ? max_ctas : sm_count()) / 2;
+  if (cap < 1) return cudaErrorInvalidValue;
+  plan.grid = 2 * (units < cap ? units : cap);
   return cudaSuccess;
 }
 
@@ -570,6 +610,10 @@ cudaError_t launch_tc(const TcPlan& plan, cudaStream_t s, LaunchOpts opts) {
   if (plan.mode == 3) {
     return plan.dtype == DType::BF16 ? launch_halo_pair_t<__nv_bfloat16>(plan, s, opts)
                                      : launch_halo_pair_t<__half>(plan, s, opts);
+  }
+  if (plan.mode == 5) {
+    return plan.dtype == DType::BF16 ? launch_lateral_pair_t<__nv_bfloat16>(plan, s, opts)
+                                     : launch_lateral_pair_t<__half>(plan, s, opts);
   }
   if (plan.mode == 0) {
     return plan.dtype == DType::BF16 ? launch_t<0, __nv_bfloat16>(plan, s, opts)

@@ -69,6 +69,9 @@ SIGNATURES = {
     "ufpn_lateral_conv": (
         c_int, [c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                 c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p]),
+    "ufpn_lateral_conv_pair": (
+        c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
+                c_int, c_int, c_void_p]),
     "ufpn_conv3x3": (
         c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
     "ufpn_upsample_add": (

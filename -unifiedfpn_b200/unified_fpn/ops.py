@@ -48,7 +48,7 @@ def _check_cuda(*ts):
 
 
 def fpn_lateral_conv(input: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor,
-                     coarse: torch.Tensor | None = None) -> torch.Tensor:
+                     coarse: torch.Tensor | None = None, cta_pair: bool = False) -> torch.Tensor:
     """1x1 lateral conv + bias, optionally fused with the top-down upsample-add:
     ``out = conv1x1(input, weight) + bias [+ bilinear_upsample(coarse, input size)]``.
 
@@ -56,6 +56,7 @@ def fpn_lateral_conv(input: torch.Tensor, weight: torch.Tensor, bias: torch.Tens
     lateral_conv_kernel (lib/kernels/compute/fpn_compute_kernels.cu:127-230).
     ``weight`` is [Cout, Cin] or [Cout, Cin, 1, 1]; ``bias`` [Cout] (fp32).
     fp32 input: NCHW, any Cout.  16-bit input: channels_last, Cout = 256.
+    ``cta_pair`` (16-bit, Cin <= 256): the CTA-pair kernel with resident weights.
     """
     _check_cuda(input, weight, bias, coarse)
     if input.dim() != 4:
@@ -81,6 +82,14 @@ def fpn_lateral_conv(input: torch.Tensor, weight: torch.Tensor, bias: torch.Tens
                                    else torch.contiguous_format)
         Hc, Wc = coarse.shape[2], coarse.shape[3]
     out = _empty_like_layout((N, Cout, H, W), input, lay)
+    if cta_pair:
+        if dt == _lib.DTYPE_F32 or Cout != 256:
+            raise ValueError("the CTA-pair lateral takes bf16 / fp16 input and Cout = 256")
+        check(lib.ufpn_lateral_conv_pair(dt, input.data_ptr(), w.data_ptr(), b.data_ptr(),
+                                         coarse.data_ptr() if coarse is not None else None,
+                                         out.data_ptr(), N, Cin, H, W, Hc, Wc, _stream(input)),
+              "ufpn_lateral_conv_pair")
+        return out
     check(lib.ufpn_lateral_conv(dt, lay, input.data_ptr(), w.data_ptr(), b.data_ptr(),
                                 coarse.data_ptr() if coarse is not None else None, out.data_ptr(),
                                 N, Cin, H, W, Cout, Hc, Wc, _stream(input)), "ufpn_lateral_conv")

@@ -135,7 +135,7 @@ struct TcPlan {
   alignas(64) CUtensorMap map_coarse;
   unsigned char args[256];  // TcGemmArgs, opaque outside tc_kernels.cu
   int mode = 0;  // 0 lateral, 1 conv3x3, 2 conv3x3 halo, 3 halo on CTA pairs, 4 the same + e4m3
-                 // quantisation of a bf16 input in shared memory
+                 // quantisation of a bf16 input in shared memory, 5 lateral on CTA pairs
   DType dtype = DType::BF16;
   int grid = 0;
   int num_tiles = 0;
@@ -176,6 +176,13 @@ cudaError_t plan_tc_lateral(TcPlan& plan, DType dt, const void* x, const void* w
                             int max_ctas, const TcScales& scales = TcScales());
 // 3x3 pad-1 conv, 256 -> 256: x NHWC [N][H][W][256]; w: [256][9][256]; out NHWC;
 // p6 (optional) NHWC [N][ceil(H/2)][ceil(W/2)][256].  E4M3 requires the halo tiling.
+// The 16-bit lateral on CTA pairs (lateral_pair.cuh): each CTA keeps half of the weights
+// resident (Cin <= 256) and adds the top-down taps from a staged coarse box in its epilogue
+// (the box must fit 64 coarse pixels).  cudaErrorNotSupported when those do not hold.
+cudaError_t plan_tc_lateral_pair(TcPlan& plan, DType dt, const void* x, const void* w,
+                                 const float* bias, const void* coarse, void* out, int N,
+                                 int Cin, int H, int W, int Hc, int Wc, Conv3x3Tiling tiling,
+                                 int* status, int max_ctas = 0);
 cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w,
                             const float* bias, void* out, void* p6, int N, int H, int W,
                             Conv3x3Tiling tiling, int* status, int max_ctas,

@@ -125,6 +125,14 @@ int ufpn_core_device_status(ufpn_core* core, int reset, int* status_out);
 int ufpn_lateral_conv(int dtype, int layout, const void* x, const void* w, const float* bias,
                       const void* coarse, void* out, int N, int Cin, int H, int W, int Cout,
                       int Hc, int Wc, void* stream);
+/* The same 16-bit lateral (NHWC, Cout = 256) on CTA pairs with each SM's half of the weights
+ * resident in shared memory (tcgen05 cta_group::2); needs Cin <= 256 and, with a coarse map,
+ * a top-down tap box of at most 64 coarse pixels per tile (UFPN_ERR_UNSUPPORTED otherwise).
+ * The top-down taps are added to the fp32 accumulator in the epilogue, so results agree with
+ * ufpn_lateral_conv to within one bf16 rounding. */
+int ufpn_lateral_conv_pair(int dtype, const void* x, const void* w, const float* bias,
+                           const void* coarse, void* out, int N, int Cin, int H, int W, int Hc,
+                           int Wc, void* stream);
 
 /* 3x3 pad-1 output conv 256->256 (+ optional P6 = P5[::2, ::2]).
  * Replaces launch_output_conv / depthwise_conv_kernel (fpn_engine.cu:315-362,

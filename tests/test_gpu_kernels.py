@@ -176,6 +176,53 @@ def test_lateral_tc_fused_upsample_add(cuda_device, dtype, geom):
     assert U.device_status() == 0
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("geom", [
+    ((2, 256, 200, 304), (100, 152)),  # R50 800x1216 P2 lateral (950 tiles, even)
+    ((1, 256, 20, 30), (10, 15)),      # odd tile count: the pair's second tile is virtual
+    ((3, 192, 40, 61), (20, 31)),      # ragged tiles, ratio not exactly 2
+    ((2, 64, 9, 5), (9, 5)),           # scale 1, one k-block
+    ((1, 256, 33, 40), None),          # no top-down add
+])
+def test_lateral_cta_pair(cuda_device, dtype, geom):
+    """The CTA-pair lateral (resident weight halves, fp32 epilogue taps) against the oracle:
+    one rounding of the fp32 result to the 16-bit output (the single-CTA lateral's tensor-core
+    top-down add uses 16-bit bilinear weights, so it is only within the looser tolerance)."""
+    import unified_fpn as U
+    (n, cin, h, w), cg = geom
+    g = torch.Generator().manual_seed(cin + h + w)
+    x = torch.randn(n, cin, h, w, generator=g).to(dtype)
+    wt = torch.randn(256, cin, generator=g) * (2.0 / cin) ** 0.5
+    b = torch.rand(256, generator=g) * 0.2 - 0.1
+    coarse = torch.randn(n, 256, *cg, generator=g).to(dtype) if cg else None
+    args = (_cl(x.to(cuda_device)), wt.to(cuda_device), b.to(cuda_device))
+    cd = _cl(coarse.to(cuda_device)) if cg else None
+    y = U.fpn_lateral_conv(*args, coarse=cd, cta_pair=True)
+    torch.cuda.synchronize()
+    assert U.device_status() == 0
+    ref = O.lateral_conv(x.float(), wt.to(dtype).float(), b)
+    if cg:
+        ref = ref + O.bilinear_upsample_t(coarse.float(), (h, w))
+    assert O.rel_err(y.cpu(), ref) < BF16_TOL
+    ulp = ref.abs() * (2.0 ** -8 if dtype == torch.bfloat16 else 2.0 ** -11)  # half an ulp, at most
+    assert ((y.cpu().float() - ref).abs() <= 2.01 * ulp + 1e-5 * ref.abs().max()).all()
+
+
+def test_lateral_cta_pair_unsupported_raises(cuda_device):
+    """Cin > 256 (weights no longer fit resident) and tiles whose tap box exceeds 64 coarse
+    pixels are refused, not computed wrongly."""
+    import unified_fpn as U
+    x = _cl(torch.randn(1, 512, 16, 16, device=cuda_device, dtype=torch.bfloat16))
+    with pytest.raises(U.UFPNError):
+        U.fpn_lateral_conv(x, torch.randn(256, 512, device=cuda_device), torch.zeros(256, device=cuda_device),
+                           cta_pair=True)
+    x = _cl(torch.randn(1, 64, 41, 57, device=cuda_device, dtype=torch.bfloat16))
+    c = _cl(torch.randn(1, 256, 21, 29, device=cuda_device, dtype=torch.bfloat16))
+    with pytest.raises(U.UFPNError):
+        U.fpn_lateral_conv(x, torch.randn(256, 64, device=cuda_device), torch.zeros(256, device=cuda_device),
+                           coarse=c, cta_pair=True)
+
+
 def test_lateral_fp32_config1(cuda_device):
     """Single-level fused op, fp32 NCHW b1: conv1x1(C3 [1,512,64,64]) + up2x(P4 [1,256,32,32])."""
     import unified_fpn as U
