@@ -28,7 +28,7 @@ LIB = PKG / "unified_fpn" / "libunified_fpn_b200.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden",
               "--expt-relaxed-constexpr", f"-I{INCLUDE}", f"-I{CSRC}"]
-SOURCES = ["tc_kernels.cu", "simt_kernels.cu", "engine.cu", "capi.cpp", "noalloc.cu"]
+SOURCES = ["tc_kernels.cu", "simt_kernels.cu", "backward.cu", "engine.cu", "capi.cpp", "noalloc.cu"]
 
 
 def nvcc() -> str:

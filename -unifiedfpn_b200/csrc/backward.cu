@@ -1,0 +1,626 @@
+// Backward pass of the FPN neck's hot path (the training consumer of the same kernels).
+//
+// Reference: src/training/backward/lateral_conv_backward.cu:7-143 (1x1 lateral: grad input,
+// grad weights, grad bias) and src/training/backward/upsample_backward.cu:4-80 (upsample-add:
+// grad lateral = grad out, grad coarse = bilinear transpose of grad out).  The reference's
+// kernels scatter with atomics (nondeterministic) and its upsample backward samples the
+// coarse map without the forward's clamp of the source coordinate to [0, in-1] (so it is not
+// the adjoint of its forward at the borders); everything here is the exact adjoint of this
+// library's forward, computed deterministically:
+//
+//   * weight gradients, dW[o][tap][c] = sum_p dY[p][o] X[p + tap][c] (1x1: one tap; 3x3: the
+//     nine taps of pad-1), are a tensor-core GEMM over pixels: fpn_dw_gemm_kernel, M = 128
+//     output channels x N = 256 input channels per CTA, K = 64-pixel k-blocks fetched by TMA
+//     as (64 channels x 64 pixels) boxes of the NHWC maps -- for both operands the channels
+//     are contiguous, i.e. MN-major operands, read through MN-major 128-byte-swizzle
+//     descriptors; the 3x3 taps shift the X box (TMA zero-fills outside the image = pad 1).
+//     The pixel range is split over CTAs (split-K); each CTA writes its fp32 partial and
+//     reduce_partials_kernel adds the partials in a fixed order.
+//   * bias gradients: column sums of dY in fp32, per block then in a fixed order.
+//   * input gradients reuse the forward kernels: the 1x1 lateral with the transposed weights
+//     (one 256-channel slice of dX per launch) and the 3x3 with the weights transposed in
+//     channels and flipped in space (dX = conv3x3(dY, W'), W'[c][8 - t][o] = W[o][t][c]).
+//   * the top-down add's adjoint, upsample_adjoint_kernel, gathers for every coarse pixel the
+//     bilinear weights of the fine pixels that tapped it (the forward's clamped taps), and P6's
+//     adjoint adds dP6 into dP5's even pixels.
+#include "kernels.h"
+#include "tc_gemm.cuh"
+
+#include <cstring>
+
+namespace ufpn {
+
+namespace {
+
+// ------------------------------------------------------------------ weight gradient GEMM
+constexpr int kDwStages = 4;
+constexpr int kDwChunk = 64 * 128;         // one 64-channel x 64-pixel box, 16-bit: 8 KB
+constexpr int kDwAStage = 2 * kDwChunk;    // 128 output channels
+constexpr int kDwBStage = 4 * kDwChunk;    // 256 input channels
+constexpr int kDwOffB = kDwStages * kDwAStage;
+constexpr int kDwOffBars = kDwOffB + kDwStages * kDwBStage;
+constexpr int kDwSmemBytes = kDwOffBars + 256 + 1024;
+static_assert(kDwSmemBytes <= 232448, "dW smem");
+constexpr int kDevTimeoutDw = 0x106;
+
+struct DwArgs {
+  int tiles_x, tiles_y, N_img, kw, kh;  // 64-pixel k-blocks: kw x kh boxes over (W, H, N)
+  int num_kb, per_kb, ksplit;
+  int c_blocks, taps;
+  int Cin;
+  float* partial;  // [ksplit][taps][256][Cin]
+  int* status;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    fpn_dw_gemm_kernel(const __grid_constant__ CUtensorMap map_g,
+                       const __grid_constant__ CUtensorMap map_x, const DwArgs a) {
+  constexpr int S = kDwStages;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint8_t* smem_a = smem;
+  uint8_t* smem_b = smem + kDwOffB;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kDwOffBars);
+  uint64_t* full_bar = bars;
+  uint64_t* empty_bar = bars + S;
+  uint64_t* accf_bar = bars + 2 * S;
+  uint64_t* done_bar = accf_bar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  // work unit: (tap, 128-channel output block, 256-channel input block, pixel split)
+  int r = static_cast<int>(blockIdx.x);
+  const int split = r % a.ksplit;
+  r /= a.ksplit;
+  const int cb = r % a.c_blocks;
+  r /= a.c_blocks;
+  const int ob = r % 2;
+  const int tap = r / 2;
+  const int dy = a.taps == 9 ? tap / 3 - 1 : 0;
+  const int dx = a.taps == 9 ? tap % 3 - 1 : 0;
+  const int kb0 = split * a.per_kb;
+  const int kb1 = min(a.num_kb, kb0 + a.per_kb);  // non-empty (host)
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(accf_bar, 1);
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&map_g);
+    prefetch_tmap(&map_x);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTcBlockN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0, issued = 0;
+      uint32_t phase = 0;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, a.status, kDevTimeoutDw)) break;
+        const int tx = kb % a.tiles_x;
+        const int t2 = kb / a.tiles_x;
+        const int ty = t2 % a.tiles_y;
+        const int n = t2 / a.tiles_y;
+        const int x0 = tx * a.kw, y0 = ty * a.kh;
+        mbar_arrive_expect_tx(&full_bar[stage], kDwAStage + kDwBStage);
+        for (int j = 0; j < 2; ++j)
+          tma_load_4d(smem_a + stage * kDwAStage + j * kDwChunk, &map_g, &full_bar[stage],
+                      ob * 128 + j * 64, x0, y0, n, kPolicyEvictFirst);
+        for (int j = 0; j < 4; ++j)
+          tma_load_4d(smem_b + stage * kDwBStage + j * kDwChunk, &map_x, &full_bar[stage],
+                      cb * 256 + j * 64, x0 + dx, y0 + dy, n, kPolicyEvictFirst);
+        ++issued;
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      griddep_launch_dependents();
+      for (int i = 0; i < S && i < issued; ++i) {
+        if (--stage < 0) {
+          stage = S - 1;
+          phase ^= 1u;
+        }
+        mbar_wait_drain(&full_bar[stage], phase);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // both operands MN-major: channels contiguous, pixels (K) across 128-byte rows
+      constexpr uint32_t idesc =
+          make_idesc(kTcBlockM, kTcBlockN, TcElem<T>::kFmt, TcElem<T>::kFmt, 1u, 1u);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&full_bar[stage], phase, abort_flag, a.status, kDevTimeoutDw)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t adesc = sdesc_mnmajor_sw128(smem_u32(smem_a + stage * kDwAStage), kDwChunk);
+        const uint64_t bdesc = sdesc_mnmajor_sw128(smem_u32(smem_b + stage * kDwBStage), kDwChunk);
+#pragma unroll
+        for (int k = 0; k < kMmaPerKb; ++k)  // +16 pixel rows (2048 bytes) per MMA step
+          tc_mma<T>(tmem_base, adesc + 128u * k, bdesc + 128u * k, idesc,
+                    (kb > kb0 || k > 0) ? 1u : 0u);
+        tc_commit(&empty_bar[stage]);
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (ok) tc_commit(accf_bar);
+      tc_commit(done_bar);
+      mbar_wait_drain(done_bar, 0);
+    }
+  } else {
+    // epilogue: TMEM lane = output channel o, column = input channel c; fp32 partial rows
+    const int quarter = warp & 3;
+    const int chalf = (warp - 2) >> 2;
+    const int o = ob * 128 + quarter * 32 + lane;
+    const bool ok = mbar_wait(accf_bar, 0, abort_flag, a.status, kDevTimeoutDw);
+    if (__all_sync(0xffffffffu, ok)) {
+      tc_fence_after();
+      float* row = a.partial +
+                   ((static_cast<size_t>(split) * a.taps + tap) * 256 + o) * a.Cin;
+#pragma unroll 1
+      for (int h = 0; h < 4; ++h) {
+        const int col = chalf * 128 + h * 32;
+        uint32_t v[32];
+        tmem_ld32(tmem_base + static_cast<uint32_t>(col) + (static_cast<uint32_t>(quarter * 32) << 16),
+                  v);
+        tmem_wait_ld();
+        const int c0 = cb * 256 + col;
+        if (c0 + 32 <= a.Cin && (a.Cin & 3) == 0) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            reinterpret_cast<float4*>(row + c0)[i] =
+                make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                            __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (c0 + i < a.Cin) row[c0 + i] = __uint_as_float(v[i]);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTcBlockN);
+  }
+}
+
+// out[(o * taps + t) * Cin + c] = sum over s (in order) of partial[s][t][o][c]
+__global__ void __launch_bounds__(256) reduce_partials_kernel(const float* __restrict__ partial,
+                                                              float* __restrict__ out, int ksplit,
+                                                              int taps, int Cin) {
+  const long long per = static_cast<long long>(taps) * 256 * Cin;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < per;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < ksplit; ++s) acc += partial[s * per + i];
+    const int c = static_cast<int>(i % Cin);
+    const long long to = i / Cin;
+    const int o = static_cast<int>(to % 256);
+    const int t = static_cast<int>(to / 256);
+    out[(static_cast<size_t>(o) * taps + t) * Cin + c] = acc;
+  }
+}
+
+// ------------------------------------------------------------------ bias gradient
+template <typename T>
+__device__ __forceinline__ float bw_to_f(T v) {
+  return static_cast<float>(v);
+}
+template <>
+__device__ __forceinline__ float bw_to_f<__half>(__half v) {
+  return __half2float(v);
+}
+template <>
+__device__ __forceinline__ float bw_to_f<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+template <typename T>
+__device__ __forceinline__ T bw_from_f(float v);
+template <>
+__device__ __forceinline__ float bw_from_f<float>(float v) {
+  return v;
+}
+template <>
+__device__ __forceinline__ __half bw_from_f<__half>(float v) {
+  return __float2half_rn(v);
+}
+template <>
+__device__ __forceinline__ __nv_bfloat16 bw_from_f<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+// part[b][c] = sum of g[p][c] over the pixels p of block b's contiguous run (thread = channel)
+template <typename T>
+__global__ void __launch_bounds__(256) colsum_kernel(const T* __restrict__ g, long long pixels,
+                                                     int C, long long per, float* __restrict__ part) {
+  const long long p0 = static_cast<long long>(blockIdx.x) * per;
+  const long long p1 = min(pixels, p0 + per);
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    float acc = 0.f;
+    for (long long p = p0; p < p1; ++p) acc += bw_to_f(g[p * C + c]);
+    part[static_cast<size_t>(blockIdx.x) * C + c] = acc;
+  }
+}
+__global__ void __launch_bounds__(256) sum_rows_kernel(const float* __restrict__ part, int rows,
+                                                       int C, float* __restrict__ out) {
+  const int c = static_cast<int>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  float acc = 0.f;
+  for (int r = 0; r < rows; ++r) acc += part[static_cast<size_t>(r) * C + c];
+  out[c] = acc;
+}
+
+// ------------------------------------------------------------------ top-down adjoint
+__device__ __forceinline__ float bw_src(int o, int in, float scale) {
+  const float s = (static_cast<float>(o) + 0.5f) * scale - 0.5f;
+  return fminf(fmaxf(s, 0.f), static_cast<float>(in - 1));
+}
+// weight with which fine coordinate o (of `out`) taps coarse coordinate q (of `in`)
+__device__ __forceinline__ float bw_tap_weight(int o, int q, int in, float scale) {
+  const float s = bw_src(o, in, scale);
+  const int a = static_cast<int>(s);
+  const int b = min(a + 1, in - 1);
+  const float w = s - static_cast<float>(a);
+  return (a == q ? 1.f - w : 0.f) + (b == q ? w : 0.f);
+}
+
+// out[n, yc, xc, :] = base[n, yc, xc, :] (or 0) + sum over fine (y, x) of
+// wy(y, yc) * wx(x, xc) * g[n, y, x, :]  -- NHWC, C a multiple of 16 / sizeof(T).
+// One warp per coarse pixel, lanes over 16-byte channel vectors.
+template <typename T>
+__global__ void __launch_bounds__(256) upsample_adjoint_kernel(
+    const T* __restrict__ g, const T* base, T* out, int N, int C, int Hc, int Wc, int H, int W,
+    float sy, float sx) {
+  constexpr int V = 16 / sizeof(T);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long pix = static_cast<long long>(blockIdx.x) * 8 + warp;
+  if (pix >= static_cast<long long>(N) * Hc * Wc) return;
+  const int xc = static_cast<int>(pix % Wc);
+  const long long t = pix / Wc;
+  const int yc = static_cast<int>(t % Hc);
+  const int n = static_cast<int>(t / Hc);
+  // fine rows / columns whose taps can reach (yc, xc): a superset, weights decide
+  const float iy = 1.f / sy, ix = 1.f / sx;
+  const int y_lo = max(0, static_cast<int>(floorf((yc - 1 + 0.5f) * iy - 0.5f)) - 1);
+  const int y_hi = min(H - 1, static_cast<int>(ceilf((yc + 1 + 0.5f) * iy - 0.5f)) + 1);
+  const int x_lo = max(0, static_cast<int>(floorf((xc - 1 + 0.5f) * ix - 0.5f)) - 1);
+  const int x_hi = min(W - 1, static_cast<int>(ceilf((xc + 1 + 0.5f) * ix - 0.5f)) + 1);
+  const bool y_edge = yc == Hc - 1, x_edge = xc == Wc - 1;  // clamped tails reach the edge
+  const int y_end = y_edge ? H - 1 : y_hi;
+  const int x_end = x_edge ? W - 1 : x_hi;
+  const T* gn = g + static_cast<size_t>(n) * H * W * C;
+  const size_t ob = (static_cast<size_t>(n) * Hc * Wc + static_cast<size_t>(yc) * Wc + xc) * C;
+  for (int cv = lane; cv * V < C; cv += 32) {
+    float acc[V];
+#pragma unroll
+    for (int e = 0; e < V; ++e) acc[e] = 0.f;
+    for (int y = y_lo; y <= y_end; ++y) {
+      const float wy = bw_tap_weight(y, yc, Hc, sy);
+      if (wy == 0.f) continue;
+      for (int x = x_lo; x <= x_end; ++x) {
+        const float wx = bw_tap_weight(x, xc, Wc, sx);
+        if (wx == 0.f) continue;
+        const float w = wy * wx;
+        union {
+          uint4 u;
+          T e[V];
+        } v;
+        v.u = __ldg(reinterpret_cast<const uint4*>(gn + (static_cast<size_t>(y) * W + x) * C) + cv);
+#pragma unroll
+        for (int e = 0; e < V; ++e) acc[e] = fmaf(bw_to_f(v.e[e]), w, acc[e]);
+      }
+    }
+    union {
+      uint4 u;
+      T e[V];
+    } o;
+    if (base) {
+      union {
+        uint4 u;
+        T e[V];
+      } b;
+      b.u = *(reinterpret_cast<const uint4*>(base + ob) + cv);
+#pragma unroll
+      for (int e = 0; e < V; ++e) o.e[e] = bw_from_f<T>(bw_to_f(b.e[e]) + acc[e]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < V; ++e) o.e[e] = bw_from_f<T>(acc[e]);
+    }
+    *(reinterpret_cast<uint4*>(out + ob) + cv) = o.u;
+  }
+}
+
+// dP5[n, 2y, 2x, :] += dP6[n, y, x, :] (NHWC, 16-byte vectors)
+template <typename T>
+__global__ void __launch_bounds__(256) p6_adjoint_kernel(const T* __restrict__ g6, T* g5, int N,
+                                                         int C, int H5, int W5) {
+  constexpr int V = 16 / sizeof(T);
+  const int H6 = (H5 - 1) / 2 + 1, W6 = (W5 - 1) / 2 + 1;
+  const long long total = static_cast<long long>(N) * H6 * W6 * (C / V);
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int cv = static_cast<int>(i % (C / V));
+    const long long p = i / (C / V);
+    const int x = static_cast<int>(p % W6);
+    const long long q = p / W6;
+    const int y = static_cast<int>(q % H6);
+    const int n = static_cast<int>(q / H6);
+    union {
+      uint4 u;
+      T e[V];
+    } a, b;
+    a.u = __ldg(reinterpret_cast<const uint4*>(g6 + (static_cast<size_t>(p) * C)) + cv);
+    uint4* dst = reinterpret_cast<uint4*>(
+                     g5 + ((static_cast<size_t>(n) * H5 + 2 * y) * W5 + 2 * x) * C) + cv;
+    b.u = *dst;
+#pragma unroll
+    for (int e = 0; e < V; ++e) b.e[e] = bw_from_f<T>(bw_to_f(b.e[e]) + bw_to_f(a.e[e]));
+    *dst = b.u;
+  }
+}
+
+// ------------------------------------------------------------------ weight layouts
+// out[c][r] = in[r][c] for an R x C matrix (rows of out beyond C up to out_rows are zeroed)
+template <typename T>
+__global__ void __launch_bounds__(256) transpose_kernel(const T* __restrict__ in, T* __restrict__ out,
+                                                        int R, int C, int out_rows) {
+  const long long total = static_cast<long long>(out_rows) * R;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(i % R);
+    const int c = static_cast<int>(i / R);
+    out[i] = c < C ? in[static_cast<size_t>(r) * C + c] : bw_from_f<T>(0.f);
+  }
+}
+// packed 3x3 weights [256 o][9 t][256 c] -> [256 c][9 t'][256 o], t' = 8 - t
+template <typename T>
+__global__ void __launch_bounds__(256) flip_conv3x3_kernel(const T* __restrict__ in,
+                                                           T* __restrict__ out) {
+  const int total = 256 * 9 * 256;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int o = i % 256;
+    const int tp = (i / 256) % 9;
+    const int c = i / (256 * 9);
+    out[i] = in[(static_cast<size_t>(o) * 9 + (8 - tp)) * 256 + c];
+  }
+}
+
+// 64-pixel k-block shape with the fewest padded pixels
+void dw_block_shape(int H, int W, int& kw, int& kh) {
+  long long best = -1;
+  for (int w : {64, 32, 16, 8}) {
+    const int h = 64 / w;
+    const long long area = static_cast<long long>((W + w - 1) / w) * w * ((H + h - 1) / h) * h;
+    if (best < 0 || area < best) {
+      best = area;
+      kw = w;
+      kh = h;
+    }
+  }
+}
+
+int grid_for(long long work, int block) {
+  const long long g = (work + block - 1) / block;
+  return static_cast<int>(g < 148LL * 32 ? (g > 0 ? g : 1) : 148LL * 32);
+}
+
+}  // namespace
+
+size_t dw_gemm_workspace_bytes(int N, int H, int W, int Cin, int taps) {
+  if (N <= 0 || H <= 0 || W <= 0 || Cin <= 0 || (taps != 1 && taps != 9)) return 0;
+  int kw = 64, kh = 1;
+  dw_block_shape(H, W, kw, kh);
+  const int num_kb = ((W + kw - 1) / kw) * ((H + kh - 1) / kh) * N;
+  const int c_blocks = (Cin + 255) / 256;
+  const int units = taps * 2 * c_blocks;
+  // pixel splits: about two CTAs per SM over all units, at least 4 k-blocks per split
+  int ksplit = (2 * sm_count() + units - 1) / units;
+  ksplit = ksplit < num_kb / 4 ? ksplit : (num_kb / 4 > 0 ? num_kb / 4 : 1);
+  const int per = (num_kb + ksplit - 1) / ksplit;
+  ksplit = (num_kb + per - 1) / per;
+  return static_cast<size_t>(ksplit) * taps * 256 * Cin * sizeof(float);
+}
+
+cudaError_t launch_dw_gemm(DType dt, const void* grad_out, const void* x, int N, int H, int W,
+                           int Cin, int taps, float* grad_w, float* workspace, size_t ws_bytes,
+                           int* status, cudaStream_t s) {
+  if (dt != DType::BF16 && dt != DType::F16) return cudaErrorNotSupported;
+  if (N <= 0 || H <= 0 || W <= 0 || Cin <= 0 || Cin % 8 != 0 || (taps != 1 && taps != 9))
+    return cudaErrorInvalidValue;
+  if (!grad_out || !x || !grad_w || !workspace) return cudaErrorInvalidValue;
+  DwArgs a;
+  std::memset(&a, 0, sizeof(a));
+  dw_block_shape(H, W, a.kw, a.kh);
+  a.tiles_x = (W + a.kw - 1) / a.kw;
+  a.tiles_y = (H + a.kh - 1) / a.kh;
+  a.N_img = N;
+  a.num_kb = a.tiles_x * a.tiles_y * N;
+  a.c_blocks = (Cin + 255) / 256;
+  a.taps = taps;
+  a.Cin = Cin;
+  const int units = taps * 2 * a.c_blocks;
+  int ksplit = (2 * sm_count() + units - 1) / units;
+  ksplit = ksplit < a.num_kb / 4 ? ksplit : (a.num_kb / 4 > 0 ? a.num_kb / 4 : 1);
+  a.per_kb = (a.num_kb + ksplit - 1) / ksplit;
+  a.ksplit = (a.num_kb + a.per_kb - 1) / a.per_kb;  // every split non-empty
+  a.partial = workspace;
+  a.status = status;
+  if (static_cast<size_t>(a.ksplit) * taps * 256 * Cin * sizeof(float) > ws_bytes)
+    return cudaErrorInvalidValue;
+  CUtensorMap map_g, map_x;
+  cudaError_t e = encode_nhwc_map(&map_g, dt, grad_out, N, H, W, 256, 256, a.kw, a.kh);
+  if (e != cudaSuccess) return e;
+  if ((e = encode_nhwc_map(&map_x, dt, x, N, H, W, Cin, Cin, a.kw, a.kh)) != cudaSuccess) return e;
+  static bool configured[2][64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int ti = dt == DType::BF16 ? 0 : 1;
+  auto kern = dt == DType::BF16 ? fpn_dw_gemm_kernel<__nv_bfloat16> : fpn_dw_gemm_kernel<__half>;
+  if (dev < 64 && !configured[ti][dev]) {
+    if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  kDwSmemBytes)) != cudaSuccess)
+      return e;
+    configured[ti][dev] = true;
+  }
+  const int grid = units * a.ksplit;
+  e = launch_ex(kern, dim3(grid), dim3(kTcThreads), kDwSmemBytes, s, LaunchOpts(), 1, map_g, map_x,
+                a);
+  if (e != cudaSuccess) return e;
+  const long long per = static_cast<long long>(taps) * 256 * Cin;
+  return launch_ex(reduce_partials_kernel, dim3(grid_for(per, 256)), dim3(256), 0, s, LaunchOpts(),
+                   1, static_cast<const float*>(workspace), grad_w, a.ksplit, taps, Cin);
+}
+
+size_t colsum_workspace_bytes(long long pixels, int C) {
+  const long long blocks = pixels < 1024 ? (pixels > 0 ? pixels : 1) : 1024;
+  return static_cast<size_t>(blocks) * C * sizeof(float);
+}
+
+cudaError_t launch_colsum(DType dt, const void* g, long long pixels, int C, float* out,
+                          float* workspace, size_t ws_bytes, cudaStream_t s) {
+  if (pixels <= 0 || C <= 0 || !g || !out || !workspace) return cudaErrorInvalidValue;
+  const long long blocks = pixels < 1024 ? pixels : 1024;
+  const long long per = (pixels + blocks - 1) / blocks;
+  const int nb = static_cast<int>((pixels + per - 1) / per);
+  if (static_cast<size_t>(nb) * C * sizeof(float) > ws_bytes) return cudaErrorInvalidValue;
+  cudaError_t e;
+  switch (dt) {
+    case DType::F32:
+      e = launch_ex(colsum_kernel<float>, dim3(nb), dim3(256), 0, s, LaunchOpts(), 1,
+                    static_cast<const float*>(g), pixels, C, per, workspace);
+      break;
+    case DType::F16:
+      e = launch_ex(colsum_kernel<__half>, dim3(nb), dim3(256), 0, s, LaunchOpts(), 1,
+                    static_cast<const __half*>(g), pixels, C, per, workspace);
+      break;
+    case DType::BF16:
+      e = launch_ex(colsum_kernel<__nv_bfloat16>, dim3(nb), dim3(256), 0, s, LaunchOpts(), 1,
+                    static_cast<const __nv_bfloat16*>(g), pixels, C, per, workspace);
+      break;
+    default:
+      return cudaErrorNotSupported;
+  }
+  if (e != cudaSuccess) return e;
+  return launch_ex(sum_rows_kernel, dim3((C + 255) / 256), dim3(256), 0, s, LaunchOpts(), 1,
+                   static_cast<const float*>(workspace), nb, C, out);
+}
+
+cudaError_t launch_upsample_adjoint(DType dt, const void* grad_fine, const void* base, void* out,
+                                    int N, int C, int Hc, int Wc, int H, int W, cudaStream_t s) {
+  if (N <= 0 || C <= 0 || Hc <= 0 || Wc <= 0 || H <= 0 || W <= 0 || !grad_fine || !out)
+    return cudaErrorInvalidValue;
+  if (Hc > H || Wc > W) return cudaErrorNotSupported;  // the forward upsamples
+  if (!aligned16(grad_fine) || !aligned16(out) || (base && !aligned16(base)))
+    return cudaErrorMisalignedAddress;
+  const int esz = dtype_size(dt);
+  if ((C * esz) % 16 != 0) return cudaErrorInvalidValue;
+  const float sy = static_cast<float>(Hc) / H, sx = static_cast<float>(Wc) / W;  // forward scales
+  const long long pixels = static_cast<long long>(N) * Hc * Wc;
+  const dim3 grid(static_cast<unsigned>((pixels + 7) / 8));
+  switch (dt) {
+    case DType::F32:
+      return launch_ex(upsample_adjoint_kernel<float>, grid, dim3(256), 0, s, LaunchOpts(), 1,
+                       static_cast<const float*>(grad_fine), static_cast<const float*>(base),
+                       static_cast<float*>(out), N, C, Hc, Wc, H, W, sy, sx);
+    case DType::F16:
+      return launch_ex(upsample_adjoint_kernel<__half>, grid, dim3(256), 0, s, LaunchOpts(), 1,
+                       static_cast<const __half*>(grad_fine), static_cast<const __half*>(base),
+                       static_cast<__half*>(out), N, C, Hc, Wc, H, W, sy, sx);
+    case DType::BF16:
+      return launch_ex(upsample_adjoint_kernel<__nv_bfloat16>, grid, dim3(256), 0, s, LaunchOpts(),
+                       1, static_cast<const __nv_bfloat16*>(grad_fine),
+                       static_cast<const __nv_bfloat16*>(base),
+                       static_cast<__nv_bfloat16*>(out), N, C, Hc, Wc, H, W, sy, sx);
+    default:
+      return cudaErrorNotSupported;
+  }
+}
+
+cudaError_t launch_p6_adjoint(DType dt, const void* grad_p6, void* grad_p5, int N, int C, int H5,
+                              int W5, cudaStream_t s) {
+  if (N <= 0 || C <= 0 || H5 <= 0 || W5 <= 0 || !grad_p6 || !grad_p5) return cudaErrorInvalidValue;
+  if (!aligned16(grad_p6) || !aligned16(grad_p5)) return cudaErrorMisalignedAddress;
+  if ((C * dtype_size(dt)) % 16 != 0) return cudaErrorInvalidValue;
+  const long long work =
+      static_cast<long long>(N) * ((H5 - 1) / 2 + 1) * ((W5 - 1) / 2 + 1) * C * dtype_size(dt) / 16;
+  const dim3 grid(grid_for(work, 256));
+  switch (dt) {
+    case DType::F32:
+      return launch_ex(p6_adjoint_kernel<float>, grid, dim3(256), 0, s, LaunchOpts(), 1,
+                       static_cast<const float*>(grad_p6), static_cast<float*>(grad_p5), N, C, H5, W5);
+    case DType::F16:
+      return launch_ex(p6_adjoint_kernel<__half>, grid, dim3(256), 0, s, LaunchOpts(), 1,
+                       static_cast<const __half*>(grad_p6), static_cast<__half*>(grad_p5), N, C, H5,
+                       W5);
+    case DType::BF16:
+      return launch_ex(p6_adjoint_kernel<__nv_bfloat16>, grid, dim3(256), 0, s, LaunchOpts(), 1,
+                       static_cast<const __nv_bfloat16*>(grad_p6),
+                       static_cast<__nv_bfloat16*>(grad_p5), N, C, H5, W5);
+    default:
+      return cudaErrorNotSupported;
+  }
+}
+
+cudaError_t launch_transpose_weights(DType dt, const void* w, void* wt, int rows, int cols,
+                                     int out_rows, cudaStream_t s) {
+  if (rows <= 0 || cols <= 0 || out_rows < cols || !w || !wt) return cudaErrorInvalidValue;
+  const dim3 grid(grid_for(static_cast<long long>(out_rows) * rows, 256));
+  switch (dt) {
+    case DType::F16:
+      return launch_ex(transpose_kernel<__half>, grid, dim3(256), 0, s, LaunchOpts(), 1,
+                       static_cast<const __half*>(w), static_cast<__half*>(wt), rows, cols, out_rows);
+    case DType::BF16:
+      return launch_ex(transpose_kernel<__nv_bfloat16>, grid, dim3(256), 0, s, LaunchOpts(), 1,
+                       static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(wt), rows,
+                       cols, out_rows);
+    default:
+      return cudaErrorNotSupported;
+  }
+}
+
+cudaError_t launch_flip_conv3x3_weights(DType dt, const void* w_packed, void* w_flipped,
+                                        cudaStream_t s) {
+  if (!w_packed || !w_flipped) return cudaErrorInvalidValue;
+  const dim3 grid(grid_for(256LL * 9 * 256, 256));
+  switch (dt) {
+    case DType::F16:
+      return launch_ex(flip_conv3x3_kernel<__half>, grid, dim3(256), 0, s, LaunchOpts(), 1,
+                       static_cast<const __half*>(w_packed), static_cast<__half*>(w_flipped));
+    case DType::BF16:
+      return launch_ex(flip_conv3x3_kernel<__nv_bfloat16>, grid, dim3(256), 0, s, LaunchOpts(), 1,
+                       static_cast<const __nv_bfloat16*>(w_packed),
+                       static_cast<__nv_bfloat16*>(w_flipped));
+    default:
+      return cudaErrorNotSupported;
+  }
+}
+
+}  // namespace ufpn

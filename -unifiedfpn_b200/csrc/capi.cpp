@@ -427,6 +427,150 @@ int ufpn_merge_two_levels(int dtype, const void* m5, const void* l4, void* m4, v
   return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "merge_two_levels");
 }
 
+namespace {
+// Stream-ordered scratch for one backward call, freed (stream-ordered) on scope exit.
+struct StreamScratch {
+  cudaStream_t s;
+  void* p = nullptr;
+  explicit StreamScratch(cudaStream_t st) : s(st) {}
+  cudaError_t alloc(size_t bytes) { return cudaMallocAsync(&p, bytes > 0 ? bytes : 16, s); }
+  ~StreamScratch() {
+    if (p) cudaFreeAsync(p, s);
+  }
+};
+bool parse_16bit(int dtype, DType* dt) {
+  return parse_dtype(dtype, dt) && (*dt == DType::BF16 || *dt == DType::F16);
+}
+}  // namespace
+
+int ufpn_lateral_conv_backward(int dtype, const void* x, const void* w, const void* grad_out,
+                               void* grad_x, float* grad_w, float* grad_b, int N, int Cin, int H,
+                               int W, void* stream) {
+  DType dt;
+  if (!parse_16bit(dtype, &dt)) return fail(UFPN_ERR_UNSUPPORTED, "backward takes bf16 or fp16");
+  if (!grad_out || (grad_x && !w) || (grad_w && !x))
+    return fail(UFPN_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (N <= 0 || Cin <= 0 || H <= 0 || W <= 0) return fail(UFPN_ERR_INVALID_ARG, "sizes must be positive");
+  if (Cin % 8 != 0) return fail(UFPN_ERR_UNSUPPORTED, "Cin must be a multiple of 8");
+  if (!ufpn::aligned16(grad_out) || (x && !ufpn::aligned16(x)) || (w && !ufpn::aligned16(w)) ||
+      (grad_x && !ufpn::aligned16(grad_x)))
+    return fail(UFPN_ERR_ALIGNMENT, "tensors must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const long long pixels = static_cast<long long>(N) * H * W;
+  const int cblk = (Cin + 255) / 256;
+  const size_t esz = ufpn::dtype_size(dt);
+  const size_t wt_bytes = grad_x ? static_cast<size_t>(cblk) * 256 * 256 * esz : 0;
+  const size_t zb_bytes = 1024;  // zero bias of the input-gradient launches
+  const size_t dw_bytes = grad_w ? ufpn::dw_gemm_workspace_bytes(N, H, W, Cin, 1) : 0;
+  const size_t cs_bytes = grad_b ? ufpn::colsum_workspace_bytes(pixels, 256) : 0;
+  StreamScratch scratch(s);
+  cudaError_t e = scratch.alloc(wt_bytes + zb_bytes + dw_bytes + cs_bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "backward scratch");
+  uint8_t* base = static_cast<uint8_t*>(scratch.p);
+  if (grad_x) {
+    void* wt = base;
+    float* zero_bias = reinterpret_cast<float*>(base + wt_bytes);
+    if ((e = cudaMemsetAsync(zero_bias, 0, zb_bytes, s)) != cudaSuccess) return cuda_fail(e, "memset");
+    if ((e = ufpn::launch_transpose_weights(dt, w, wt, 256, Cin, cblk * 256, s)) != cudaSuccess)
+      return cuda_fail(e, "transpose weights");
+    for (int cb = 0; cb < cblk; ++cb) {
+      // grad_x[:, cb*256 .. +256) = grad_out . w^T[cb*256 .. +256) : a 256-channel lateral
+      ufpn::TcPlan plan;
+      uint8_t* out = static_cast<uint8_t*>(grad_x) + static_cast<size_t>(cb) * 256 * esz;
+      const uint8_t* wslice = static_cast<const uint8_t*>(wt) + static_cast<size_t>(cb) * 256 * 256 * esz;
+      e = ufpn::plan_tc_lateral(plan, dt, grad_out, wslice, zero_bias, nullptr, out, N, 256, H, W,
+                                0, 0, ufpn::default_tiling(H, W), device_status_word(), 0);
+      if (e == cudaSuccess) e = ufpn::tc_set_output_view(plan, out, Cin - cb * 256 < 256 ? Cin - cb * 256 : 256, Cin);
+      if (e == cudaSuccess) e = ufpn::launch_tc(plan, s);
+      if (e != cudaSuccess) return cuda_fail(e, "lateral input gradient");
+    }
+  }
+  if (grad_w) {
+    float* ws = reinterpret_cast<float*>(base + wt_bytes + zb_bytes);
+    e = ufpn::launch_dw_gemm(dt, grad_out, x, N, H, W, Cin, 1, grad_w, ws, dw_bytes,
+                             device_status_word(), s);
+    if (e != cudaSuccess) return cuda_fail(e, "lateral weight gradient");
+  }
+  if (grad_b) {
+    float* ws = reinterpret_cast<float*>(base + wt_bytes + zb_bytes + dw_bytes);
+    e = ufpn::launch_colsum(dt, grad_out, pixels, 256, grad_b, ws, cs_bytes, s);
+    if (e != cudaSuccess) return cuda_fail(e, "bias gradient");
+  }
+  return UFPN_OK;
+}
+
+int ufpn_conv3x3_backward(int dtype, const void* x, const void* w, const void* grad_out,
+                          void* grad_x, float* grad_w, float* grad_b, int N, int H, int W,
+                          void* stream) {
+  DType dt;
+  if (!parse_16bit(dtype, &dt)) return fail(UFPN_ERR_UNSUPPORTED, "backward takes bf16 or fp16");
+  if (!grad_out || (grad_x && !w) || (grad_w && !x))
+    return fail(UFPN_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (N <= 0 || H <= 0 || W <= 0) return fail(UFPN_ERR_INVALID_ARG, "sizes must be positive");
+  if (!ufpn::aligned16(grad_out) || (x && !ufpn::aligned16(x)) || (w && !ufpn::aligned16(w)) ||
+      (grad_x && !ufpn::aligned16(grad_x)))
+    return fail(UFPN_ERR_ALIGNMENT, "tensors must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const long long pixels = static_cast<long long>(N) * H * W;
+  const size_t esz = ufpn::dtype_size(dt);
+  const size_t wf_bytes = grad_x ? 256ull * 9 * 256 * esz : 0;
+  const size_t zb_bytes = 1024;
+  const size_t dw_bytes = grad_w ? ufpn::dw_gemm_workspace_bytes(N, H, W, 256, 9) : 0;
+  const size_t cs_bytes = grad_b ? ufpn::colsum_workspace_bytes(pixels, 256) : 0;
+  StreamScratch scratch(s);
+  cudaError_t e = scratch.alloc(wf_bytes + zb_bytes + dw_bytes + cs_bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "backward scratch");
+  uint8_t* base = static_cast<uint8_t*>(scratch.p);
+  if (grad_x) {
+    float* zero_bias = reinterpret_cast<float*>(base + wf_bytes);
+    if ((e = cudaMemsetAsync(zero_bias, 0, zb_bytes, s)) != cudaSuccess) return cuda_fail(e, "memset");
+    if ((e = ufpn::launch_flip_conv3x3_weights(dt, w, base, s)) != cudaSuccess)
+      return cuda_fail(e, "flip weights");
+    ufpn::TcPlan plan;
+    e = ufpn::plan_tc_conv3x3(plan, dt, grad_out, base, zero_bias, grad_x, nullptr, N, H, W,
+                              ufpn::halo_tiling(), device_status_word(), 0);
+    if (e == cudaSuccess) e = ufpn::launch_tc(plan, s);
+    if (e != cudaSuccess) return cuda_fail(e, "3x3 input gradient");
+  }
+  if (grad_w) {
+    float* ws = reinterpret_cast<float*>(base + wf_bytes + zb_bytes);
+    e = ufpn::launch_dw_gemm(dt, grad_out, x, N, H, W, 256, 9, grad_w, ws, dw_bytes,
+                             device_status_word(), s);
+    if (e != cudaSuccess) return cuda_fail(e, "3x3 weight gradient");
+  }
+  if (grad_b) {
+    float* ws = reinterpret_cast<float*>(base + wf_bytes + zb_bytes + dw_bytes);
+    e = ufpn::launch_colsum(dt, grad_out, pixels, 256, grad_b, ws, cs_bytes, s);
+    if (e != cudaSuccess) return cuda_fail(e, "bias gradient");
+  }
+  return UFPN_OK;
+}
+
+int ufpn_upsample_add_backward(int dtype, const void* grad_out, const void* base,
+                               void* grad_coarse, int N, int C, int Hc, int Wc, int H, int W,
+                               void* stream) {
+  DType dt;
+  if (!parse_dtype(dtype, &dt)) return fail(UFPN_ERR_UNSUPPORTED, "unsupported dtype");
+  if (!grad_out || !grad_coarse) return fail(UFPN_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (N <= 0 || C <= 0 || Hc <= 0 || Wc <= 0 || H <= 0 || W <= 0)
+    return fail(UFPN_ERR_INVALID_ARG, "sizes must be positive");
+  if (Hc > H || Wc > W) return fail(UFPN_ERR_UNSUPPORTED, "the coarse map must not be larger");
+  cudaError_t e = ufpn::launch_upsample_adjoint(dt, grad_out, base, grad_coarse, N, C, Hc, Wc, H,
+                                                W, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "upsample_add backward");
+}
+
+int ufpn_p6_backward(int dtype, const void* grad_p6, void* grad_p5, int N, int C, int H5, int W5,
+                     void* stream) {
+  DType dt;
+  if (!parse_dtype(dtype, &dt)) return fail(UFPN_ERR_UNSUPPORTED, "unsupported dtype");
+  if (!grad_p6 || !grad_p5) return fail(UFPN_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (N <= 0 || C <= 0 || H5 <= 0 || W5 <= 0) return fail(UFPN_ERR_INVALID_ARG, "sizes must be positive");
+  cudaError_t e = ufpn::launch_p6_adjoint(dt, grad_p6, grad_p5, N, C, H5, W5,
+                                          static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "p6 backward");
+}
+
 int ufpn_p6_maxpool(int dtype, int layout, const void* p5, void* p6, int N, int C, int H, int W,
                     void* stream) {
   DType dt;

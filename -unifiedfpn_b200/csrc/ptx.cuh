@@ -389,12 +389,13 @@ __device__ __forceinline__ uint64_t sdesc_mnmajor_sw128(uint32_t saddr, uint32_t
 
 // Instruction descriptor for kind::f16 / kind::f8f6f4 with fp32 accumulation.
 // a_fmt/b_fmt: kind::f16 -> 0 = f16, 1 = bf16; kind::f8f6f4 -> 0 = e4m3, 1 = e5m2.
-// b_mn_major: B stored MN-major (N contiguous) instead of K-major.
+// b_mn_major / a_mn_major: B / A stored MN-major (N / M contiguous) instead of K-major.
 __host__ __device__ constexpr uint32_t make_idesc(int M, int N, uint32_t a_fmt, uint32_t b_fmt,
-                                                  uint32_t b_mn_major = 0) {
+                                                  uint32_t b_mn_major = 0,
+                                                  uint32_t a_mn_major = 0) {
   return (1u << 4)                                // D format: f32
          | (a_fmt << 7) | (b_fmt << 10)           // A / B formats
-         | (0u << 15) | (b_mn_major << 16)        // A K-major, B K- or MN-major
+         | (a_mn_major << 15) | (b_mn_major << 16)  // A / B K- or MN-major
          | (static_cast<uint32_t>(N >> 3) << 17)  // N / 8
          | (static_cast<uint32_t>(M >> 4) << 24); // M / 16
 }

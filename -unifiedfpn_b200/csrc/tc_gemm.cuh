@@ -155,6 +155,9 @@ struct TcGemmArgs {
   // e4m3 3x3 that quantises its bf16 input in shared memory: per-image absmax of the input
   // (fp32 bits); the activation scale is then amax[n] / 448 (ascale unused)
   const unsigned* in_amax;
+  // 16-bit output: store only columns [0, out_cols) (0 = all 256), for an output view whose
+  // channel slice is narrower than a tile (no TMA store then starts beyond the tensor)
+  int out_cols;
 };
 
 template <typename T>
@@ -561,7 +564,7 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
         if (lane == 0) {
           // e4m3: the warp's 128 channels (128 bytes per pixel) in one store.  Every buffer
           // use commits a group (empty for virtual tiles) so group counts stay in step.
-          if (real)
+          if (real && (omode != 0 || args.out_cols == 0 || col0 < args.out_cols))
             tma_store_4d(map_out, my_stage + sbuf * kTcStagingPerWarp,
                          omode == 0 ? col0 : chalf * 128, ox, oy, n);
           bulk_commit_group();

@@ -431,6 +431,35 @@ cudaError_t tc_build_wb_table(DType dt, int H, int W, int Hc, int Wc, Conv3x3Til
   return cudaGetLastError();
 }
 
+cudaError_t encode_nhwc_map(CUtensorMap* map, DType dt, const void* base, int N, int H, int W,
+                            int C, int pix_stride, int bw, int bh) {
+  if (N <= 0 || H <= 0 || W <= 0 || C <= 0 || pix_stride < C) return cudaErrorInvalidValue;
+  const uint64_t esz = static_cast<uint64_t>(dtype_size(dt));
+  uint64_t dims[4] = {static_cast<uint64_t>(C), static_cast<uint64_t>(W),
+                      static_cast<uint64_t>(H), static_cast<uint64_t>(N)};
+  uint64_t strides[3] = {static_cast<uint64_t>(pix_stride) * esz,
+                         static_cast<uint64_t>(W) * pix_stride * esz,
+                         static_cast<uint64_t>(H) * W * pix_stride * esz};
+  uint32_t box[4] = {static_cast<uint32_t>(128 / esz), static_cast<uint32_t>(bw),
+                     static_cast<uint32_t>(bh), 1};
+  return encode(map, dt, 4, base, dims, strides, box);
+}
+
+cudaError_t tc_set_output_view(TcPlan& plan, void* out, int C, int pix_stride) {
+  if (plan.mode != 0 || plan.dtype == DType::E4M3) return cudaErrorNotSupported;
+  if (!aligned16(out)) return cudaErrorMisalignedAddress;
+  TcGemmArgs a;
+  std::memcpy(&a, plan.args, sizeof(a));
+  if (C > kTcBlockN) return cudaErrorInvalidValue;
+  const int sw = a.tile_w < 32 ? a.tile_w : 32;
+  cudaError_t e = encode_nhwc_map(&plan.map_out, plan.dtype, out, a.N_img, a.H, a.W, C,
+                                  pix_stride, sw, 32 / sw);
+  if (e != cudaSuccess) return e;
+  a.out_cols = C;
+  std::memcpy(plan.args, &a, sizeof(a));
+  return cudaSuccess;
+}
+
 bool tc_attach_wb_table(TcPlan& plan, const void* table) {
   TcGemmArgs a;
   std::memcpy(&a, plan.args, sizeof(a));

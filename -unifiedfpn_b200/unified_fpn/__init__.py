@@ -9,9 +9,11 @@ that library cannot be loaded the import fails: there is no CPU fallback.
 """
 from ._lib import UFPNError, lib  # noqa: F401  (raises ImportError without the library)
 from .core import UnifiedFPN, fpn_forward_pytorch
-from .ops import (device_status, fpn_conv3x3, fpn_conv3x3_fp8, fpn_conv3x3_fp8_from_bf16, fpn_lateral_conv,
-                  fpn_lateral_conv_fp8, fpn_merge_two_levels, fpn_p6, fpn_upsample_add, fpn_upsample_bilinear,
+from .ops import (device_status, fpn_conv3x3, fpn_conv3x3_backward, fpn_conv3x3_fp8, fpn_conv3x3_fp8_from_bf16,
+                  fpn_lateral_conv, fpn_lateral_conv_backward, fpn_lateral_conv_fp8, fpn_merge_two_levels, fpn_p6,
+                  fpn_p6_backward, fpn_upsample_add, fpn_upsample_add_backward, fpn_upsample_bilinear,
                   pack_conv3x3_weight, quantize_fp8, quantize_fp8_rows)
+from .training import FPNNeck, fpn_neck_backward, fpn_neck_forward_train
 from .helpers import benchmark_fpn, check_installation, get_device_info, profile_fpn
 from .pipeline import HostPipeline
 
@@ -22,4 +24,6 @@ __all__ = [
     "fpn_upsample_add", "fpn_merge_two_levels", "fpn_p6", "fpn_conv3x3", "pack_conv3x3_weight", "device_status",
     "quantize_fp8", "quantize_fp8_rows", "fpn_lateral_conv_fp8", "fpn_conv3x3_fp8", "fpn_conv3x3_fp8_from_bf16", "HostPipeline",
     "benchmark_fpn", "profile_fpn", "get_device_info", "check_installation", "UFPNError",
+    "fpn_lateral_conv_backward", "fpn_conv3x3_backward", "fpn_upsample_add_backward", "fpn_p6_backward",
+    "FPNNeck", "fpn_neck_forward_train", "fpn_neck_backward",
 ]

@@ -185,6 +185,97 @@ def fpn_merge_two_levels(m5: torch.Tensor, l4: torch.Tensor, l3: torch.Tensor) -
     return m4, m3
 
 
+# ----------------------------------------------------------------------------- backward
+def _cl16(t: torch.Tensor, what: str) -> torch.Tensor:
+    if t.dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError(f"{what} must be bfloat16 or float16")
+    return t.contiguous(memory_format=torch.channels_last)
+
+
+def fpn_lateral_conv_backward(input: torch.Tensor, weight: torch.Tensor, grad_output: torch.Tensor,
+                              need_input_grad: bool = True):
+    """Gradients of ``fpn_lateral_conv(input, weight, bias)`` (16-bit, channels_last,
+    Cout = 256): ``(grad_input, grad_weight [256, Cin] fp32, grad_bias [256] fp32)``;
+    grad_input is None without ``need_input_grad``.  Reference: backward_lateral_conv_kernel
+    (src/training/backward/lateral_conv_backward.cu:7-143), here deterministic: the weight
+    gradient is a tensor-core GEMM over pixels, the input gradient the forward kernel with
+    the transposed weights."""
+    _check_cuda(input, weight, grad_output)
+    x = _cl16(input, "input")
+    g = _cl16(grad_output, "grad_output")
+    N, Cin, H, W = x.shape
+    if g.dtype != x.dtype or tuple(g.shape) != (N, 256, H, W):
+        raise ValueError("grad_output must be [N, 256, H, W] in the input's dtype")
+    w = weight.reshape(256, Cin).to(device=x.device, dtype=x.dtype).contiguous()
+    gx = torch.empty_like(x, memory_format=torch.channels_last) if need_input_grad else None
+    gw = torch.empty(256, Cin, device=x.device, dtype=torch.float32)
+    gb = torch.empty(256, device=x.device, dtype=torch.float32)
+    check(lib.ufpn_lateral_conv_backward(dtype_code(x), x.data_ptr(), w.data_ptr(), g.data_ptr(),
+                                         gx.data_ptr() if gx is not None else None, gw.data_ptr(),
+                                         gb.data_ptr(), N, Cin, H, W, _stream(x)),
+          "ufpn_lateral_conv_backward")
+    return gx, gw, gb
+
+
+def fpn_conv3x3_backward(input: torch.Tensor, weight: torch.Tensor, grad_output: torch.Tensor,
+                         need_input_grad: bool = True):
+    """Gradients of the 256 -> 256 pad-1 3x3 conv (``fpn_conv3x3``; 16-bit, channels_last):
+    ``(grad_input, grad_weight [256, 256, 3, 3] fp32, grad_bias [256] fp32)``.  ``weight`` is
+    [256, 256, 3, 3] (any float dtype) or packed [256, 9, 256] by ``pack_conv3x3_weight``.  The input
+    gradient is the forward 3x3 kernel with the weights transposed in channels and flipped in
+    space; the weight gradient is a tensor-core GEMM over pixels (nine shifted taps)."""
+    _check_cuda(input, weight, grad_output)
+    x = _cl16(input, "input")
+    g = _cl16(grad_output, "grad_output")
+    N, C, H, W = x.shape
+    if C != 256 or g.dtype != x.dtype or tuple(g.shape) != (N, 256, H, W):
+        raise ValueError("input and grad_output must be [N, 256, H, W] of one dtype")
+    wp = weight if (weight.dim() == 3 and weight.dtype == x.dtype) else pack_conv3x3_weight(weight, x.dtype)
+    wp = wp.contiguous()
+    gx = torch.empty_like(x, memory_format=torch.channels_last) if need_input_grad else None
+    gw = torch.empty(256, 9, 256, device=x.device, dtype=torch.float32)
+    gb = torch.empty(256, device=x.device, dtype=torch.float32)
+    check(lib.ufpn_conv3x3_backward(dtype_code(x), x.data_ptr(), wp.data_ptr(), g.data_ptr(),
+                                    gx.data_ptr() if gx is not None else None, gw.data_ptr(),
+                                    gb.data_ptr(), N, H, W, _stream(x)), "ufpn_conv3x3_backward")
+    # [o][tap][c] -> [o][c][ky][kx]
+    return gx, gw.permute(0, 2, 1).reshape(256, 256, 3, 3).contiguous(), gb
+
+
+def fpn_upsample_add_backward(grad_output: torch.Tensor, coarse_size: tuple[int, int],
+                              base: torch.Tensor | None = None) -> torch.Tensor:
+    """Gradient of the coarse input of ``fpn_upsample_add(coarse, lateral)``:
+    ``base + bilinear^T(grad_output)`` (the lateral's gradient is grad_output itself).
+    channels_last; the exact adjoint of the forward's clamped half-pixel taps.  Reference:
+    backward_upsample_add_kernel (src/training/backward/upsample_backward.cu:4-80)."""
+    _check_cuda(grad_output, base)
+    g = grad_output.contiguous(memory_format=torch.channels_last)
+    N, C, H, W = g.shape
+    Hc, Wc = coarse_size
+    out = torch.empty(N, C, Hc, Wc, device=g.device, dtype=g.dtype, memory_format=torch.channels_last)
+    if base is not None:
+        base = base.to(dtype=g.dtype).contiguous(memory_format=torch.channels_last)
+        if tuple(base.shape) != (N, C, Hc, Wc):
+            raise ValueError("base must have the coarse map's shape")
+    check(lib.ufpn_upsample_add_backward(dtype_code(g), g.data_ptr(),
+                                         base.data_ptr() if base is not None else None, out.data_ptr(),
+                                         N, C, Hc, Wc, H, W, _stream(g)), "ufpn_upsample_add_backward")
+    return out
+
+
+def fpn_p6_backward(grad_p6: torch.Tensor, grad_p5: torch.Tensor) -> torch.Tensor:
+    """Adds the gradient of P6 = P5[:, :, ::2, ::2] into ``grad_p5`` (channels_last, in place;
+    returned)."""
+    _check_cuda(grad_p6, grad_p5)
+    if not grad_p5.is_contiguous(memory_format=torch.channels_last):
+        raise ValueError("grad_p5 must be channels_last (it is updated in place)")
+    g6 = grad_p6.to(dtype=grad_p5.dtype).contiguous(memory_format=torch.channels_last)
+    N, C, H5, W5 = grad_p5.shape
+    check(lib.ufpn_p6_backward(dtype_code(grad_p5), g6.data_ptr(), grad_p5.data_ptr(), N, C, H5, W5,
+                               _stream(grad_p5)), "ufpn_p6_backward")
+    return grad_p5
+
+
 def fpn_upsample_bilinear(input: torch.Tensor, scale_factor: float) -> torch.Tensor:
     """Bilinear upsample by ``scale_factor``; output size = int(in * scale), sampled
     with scale = in / out (half-pixel, align_corners=False).

@@ -1,0 +1,133 @@
+"""Training path of the FPN neck on this library's kernels.
+
+The reference ships backward kernels for two pieces of the neck -- the 1x1 lateral
+(src/training/backward/lateral_conv_backward.cu:7-143) and the top-down upsample-add
+(src/training/backward/upsample_backward.cu:4-80) -- without a driver.  Here the whole neck
+has one: ``fpn_neck_forward_train`` runs the forward of ``UnifiedFPN`` (laterals with the fused
+top-down add, pad-1 3x3 outputs, P6) on the same tensor-core kernels and keeps what the
+backward needs; ``fpn_neck_backward`` returns the gradients of every input, weight and bias:
+
+    dP5 += P6^T(dP6);  dM_l, dW3_l, db3_l = conv3x3^T(M_l, W3_l, dP_l)       (every level)
+    dM_l += up^T(dM_{l-1}) for l = P3, P4, P5 (finest first: the top-down adjoint)
+    dC_l, dWlat_l, dblat_l = lateral^T(C_l, Wlat_l, dM_l)
+
+``FPNNeck`` wraps both in a ``torch.nn.Module`` with fp32 master weights (the kernels compute in
+the features' 16-bit dtype) for use under autograd.
+"""
+from __future__ import annotations
+
+from typing import Sequence
+
+import torch
+
+from .ops import (fpn_conv3x3, fpn_conv3x3_backward, fpn_lateral_conv, fpn_lateral_conv_backward,
+                  fpn_p6_backward, fpn_upsample_add_backward, pack_conv3x3_weight)
+
+_CL = torch.channels_last
+
+
+def fpn_neck_forward_train(feats: Sequence[torch.Tensor], lateral_w: Sequence[torch.Tensor],
+                           lateral_b: Sequence[torch.Tensor], output_w: Sequence[torch.Tensor],
+                           output_b: Sequence[torch.Tensor], return_p6: bool = True):
+    """Forward of the neck for training.  ``feats``: C2..C5 (bf16 / fp16, 4-D CUDA); weights
+    as for ``UnifiedFPN.initialize_weights`` (lateral [256, Cin], 3x3 [256, 256, 3, 3], fp32
+    biases).  Returns ``(outputs, saved)``: P2..P5 (and P6) channels_last, and the state
+    ``fpn_neck_backward`` needs (the inputs, the merged maps M2..M5, the packed weights)."""
+    if len(feats) != 4:
+        raise ValueError("feats must be C2..C5")
+    dt = feats[0].dtype
+    if dt not in (torch.bfloat16, torch.float16) or any(f.dtype != dt for f in feats):
+        raise ValueError("training runs on bf16 or fp16 features of one dtype")
+    x = [f.contiguous(memory_format=_CL) for f in feats]
+    lw = [w.reshape(256, -1).to(dtype=dt).contiguous() for w in lateral_w]
+    merged = [None] * 4
+    merged[3] = fpn_lateral_conv(x[3], lw[3], lateral_b[3])
+    for l in (2, 1, 0):  # top-down: M_l = lateral(C_l) + up(M_{l+1}), fused in the lateral
+        merged[l] = fpn_lateral_conv(x[l], lw[l], lateral_b[l], coarse=merged[l + 1])
+    packed = [pack_conv3x3_weight(w, dt) for w in output_w]
+    outs = [fpn_conv3x3(merged[l], packed[l], output_b[l]) for l in range(3)]
+    p5 = fpn_conv3x3(merged[3], packed[3], output_b[3], p6=return_p6)
+    outs += list(p5) if return_p6 else [p5]
+    return outs, {"x": x, "merged": merged, "lateral_w": lw, "packed": packed}
+
+
+def fpn_neck_backward(grad_outputs: Sequence[torch.Tensor | None], saved: dict,
+                      need_input_grad: bool = True):
+    """Gradients of the neck given dP2..dP5 (and dP6; None = zero) and ``saved`` from
+    ``fpn_neck_forward_train``.  Returns a dict: ``grad_inputs`` (dC2..dC5, or None),
+    ``grad_lateral_w`` ([256, Cin] fp32), ``grad_lateral_b``, ``grad_output_w``
+    ([256, 256, 3, 3] fp32), ``grad_output_b``."""
+    x, merged, lw, packed = saved["x"], saved["merged"], saved["lateral_w"], saved["packed"]
+    dt = x[0].dtype
+
+    def g16(g, like):
+        if g is None:
+            return torch.zeros_like(like, memory_format=_CL)
+        return g.to(dtype=dt).contiguous(memory_format=_CL)
+
+    dp = [g16(grad_outputs[l] if l < len(grad_outputs) else None, merged[l]) for l in range(4)]
+    if len(grad_outputs) > 4 and grad_outputs[4] is not None:
+        dp[3] = fpn_p6_backward(grad_outputs[4], dp[3].clone(memory_format=_CL))
+    dm, gw3, gb3 = [None] * 4, [None] * 4, [None] * 4
+    for l in range(4):
+        dm[l], gw3[l], gb3[l] = fpn_conv3x3_backward(merged[l], packed[l], dp[l])
+    for l in (1, 2, 3):  # adjoint of the top-down chain, finest first
+        dm[l] = fpn_upsample_add_backward(dm[l - 1], tuple(merged[l].shape[2:]), base=dm[l])
+    gx, gwl, gbl = [None] * 4, [None] * 4, [None] * 4
+    for l in range(4):
+        gx[l], gwl[l], gbl[l] = fpn_lateral_conv_backward(x[l], lw[l], dm[l], need_input_grad)
+    return {"grad_inputs": gx if need_input_grad else None, "grad_lateral_w": gwl,
+            "grad_lateral_b": gbl, "grad_output_w": gw3, "grad_output_b": gb3}
+
+
+class _NeckFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, return_p6, c2, c3, c4, c5, *params):
+        lw, lb, ow, ob = params[0:4], params[4:8], params[8:12], params[12:16]
+        outs, saved = fpn_neck_forward_train([c2, c3, c4, c5], lw, lb, ow, ob, return_p6)
+        ctx.saved = saved
+        ctx.weight_dtypes = [p.dtype for p in params]
+        ctx.lateral_shapes = [tuple(w.shape) for w in lw]
+        ctx.input_dtypes = [c.dtype for c in (c2, c3, c4, c5)]
+        ctx.return_p6 = return_p6
+        return tuple(outs)
+
+    @staticmethod
+    def backward(ctx, *grads):
+        need_x = any(ctx.needs_input_grad[1:5])
+        r = fpn_neck_backward(list(grads), ctx.saved, need_input_grad=need_x)
+        gx = r["grad_inputs"] if need_x else [None] * 4
+        wd = ctx.weight_dtypes
+        gl = [g.reshape(s).to(wd[i]) for i, (g, s) in enumerate(zip(r["grad_lateral_w"], ctx.lateral_shapes))]
+        gbl = [g.to(wd[4 + i]) for i, g in enumerate(r["grad_lateral_b"])]
+        gw3 = [g.to(wd[8 + i]) for i, g in enumerate(r["grad_output_w"])]
+        gb3 = [g.to(wd[12 + i]) for i, g in enumerate(r["grad_output_b"])]
+        ctx.saved = None
+        return (None, *[g.to(d) if g is not None else None for g, d in zip(gx, ctx.input_dtypes)],
+                *gl, *gbl, *gw3, *gb3)
+
+
+class FPNNeck(torch.nn.Module):
+    """Trainable FPN neck: lateral 1x1 + top-down bilinear add + pad-1 3x3 per level, P6 =
+    P5[::2, ::2], with fp32 master weights; the forward and backward run on this library's
+    kernels in the features' dtype (bf16 / fp16, channels_last), and autograd sees the usual
+    parameters."""
+
+    def __init__(self, in_channels: Sequence[int] = (256, 512, 1024, 2048), out_channels: int = 256,
+                 return_p6: bool = True, seed: int = 0):
+        super().__init__()
+        if out_channels != 256:
+            raise ValueError("the neck's kernels produce 256 channels")
+        g = torch.Generator().manual_seed(seed)
+        self.return_p6 = return_p6
+        self.lateral_w = torch.nn.ParameterList(
+            [torch.nn.Parameter(torch.randn(256, c, generator=g) * (2.0 / c) ** 0.5) for c in in_channels])
+        self.lateral_b = torch.nn.ParameterList([torch.nn.Parameter(torch.zeros(256)) for _ in in_channels])
+        self.output_w = torch.nn.ParameterList(
+            [torch.nn.Parameter(torch.randn(256, 256, 3, 3, generator=g) * (2.0 / 2304) ** 0.5)
+             for _ in in_channels])
+        self.output_b = torch.nn.ParameterList([torch.nn.Parameter(torch.zeros(256)) for _ in in_channels])
+
+    def forward(self, feats: Sequence[torch.Tensor]):
+        params = [*self.lateral_w, *self.lateral_b, *self.output_w, *self.output_b]
+        return list(_NeckFunction.apply(self.return_p6, *feats, *params))

@@ -197,6 +197,14 @@ size_t tc_wb_table_bytes(int H, int W, int Hc, int Wc, Conv3x3Tiling t);
 cudaError_t tc_build_wb_table(DType dt, int H, int W, int Hc, int Wc, Conv3x3Tiling t,
                               void* table, cudaStream_t s);
 bool tc_attach_wb_table(TcPlan& plan, const void* table);
+// Tiled NHWC tensor map with 128-byte swizzle: dims (C, W, H, N), pixel stride pix_stride
+// elements (>= C), box (one 128-byte row of channels, bw, bh, 1).
+cudaError_t encode_nhwc_map(CUtensorMap* map, DType dt, const void* base, int N, int H, int W,
+                            int C, int pix_stride, int bw, int bh);
+// 16-bit lateral plans only: store the output into channels [0, C) of a map whose pixels are
+// pix_stride elements apart (out = that channel slice's first element).  Used to write the
+// 256-channel slices of a wider tensor (the input gradient of a Cin > 256 lateral).
+cudaError_t tc_set_output_view(TcPlan& plan, void* out, int C, int pix_stride);
 // Tiling with the fewest padded pixels for an H x W map (ties: 16 wide).
 Conv3x3Tiling default_tiling(int H, int W);
 
@@ -239,6 +247,35 @@ cudaError_t plan_neck_jobs(NeckPlan& plan, DType dt, int N, const NeckLevel* lev
                            int max_ctas, unsigned long long* trace = nullptr);
 cudaError_t launch_neck(const NeckPlan& plan, cudaStream_t s, LaunchOpts opts = LaunchOpts());
 cudaError_t launch_tc(const TcPlan& plan, cudaStream_t s, LaunchOpts opts = LaunchOpts());
+
+// ---- backward pass (backward.cu).  Reference: src/training/backward/lateral_conv_backward.cu
+// :7-143 and upsample_backward.cu:4-80; here the exact adjoints of the forward, deterministic.
+// Weight gradient dW[o][t][c] = sum_p dY[p][o] X[p + shift(t)][c] (fp32, [256][taps][Cin];
+// taps 1 = the 1x1 lateral, 9 = the pad-1 3x3 with shift(t) = (t / 3 - 1, t % 3 - 1)) of
+// NHWC dY [N][H][W][256] and X [N][H][W][Cin] (16-bit): a tensor-core GEMM over pixels with
+// fp32 split-K partials in `workspace` (dw_gemm_workspace_bytes) added in a fixed order.
+size_t dw_gemm_workspace_bytes(int N, int H, int W, int Cin, int taps);
+cudaError_t launch_dw_gemm(DType dt, const void* grad_out, const void* x, int N, int H, int W,
+                           int Cin, int taps, float* grad_w, float* workspace, size_t ws_bytes,
+                           int* status, cudaStream_t s);
+// out[c] = sum over the pixels of g[p][c] (fp32; per block, then in a fixed order).
+size_t colsum_workspace_bytes(long long pixels, int C);
+cudaError_t launch_colsum(DType dt, const void* g, long long pixels, int C, float* out,
+                          float* workspace, size_t ws_bytes, cudaStream_t s);
+// Adjoint of launch_upsample_add's bilinear (NHWC, align_corners = false):
+// out = base (or 0) + up^T(grad_fine), out and base [N][Hc][Wc][C].
+cudaError_t launch_upsample_adjoint(DType dt, const void* grad_fine, const void* base, void* out,
+                                    int N, int C, int Hc, int Wc, int H, int W, cudaStream_t s);
+// Adjoint of P6 = P5[::2, ::2]: grad_p5 at even pixels += grad_p6 (NHWC, in place).
+cudaError_t launch_p6_adjoint(DType dt, const void* grad_p6, void* grad_p5, int N, int C, int H5,
+                              int W5, cudaStream_t s);
+// wt[c][r] = w[r][c] for a rows x cols matrix; rows cols..out_rows-1 of wt are zeroed.
+cudaError_t launch_transpose_weights(DType dt, const void* w, void* wt, int rows, int cols,
+                                     int out_rows, cudaStream_t s);
+// Packed 3x3 weights [256 o][9 t][256 c] -> [256 c][9 t'][256 o] with t' = 8 - t: the weights
+// of the 3x3 that computes the input gradient.
+cudaError_t launch_flip_conv3x3_weights(DType dt, const void* w_packed, void* w_flipped,
+                                        cudaStream_t s);
 
 // Number of SMs on the current device (cached).
 int sm_count();

@@ -161,6 +161,33 @@ int ufpn_upsample_add(int dtype, int layout, const void* coarse, const void* lat
 int ufpn_merge_two_levels(int dtype, const void* m5, const void* l4, void* m4, void* l3_m3, int N,
                           int H5, int W5, int H4, int W4, int H3, int W3, void* stream);
 
+/* ---- Backward pass (training).  Replaces the reference's backward_lateral_conv_kernel
+ * (src/training/backward/lateral_conv_backward.cu:7-143) and backward_upsample_add_kernel
+ * (src/training/backward/upsample_backward.cu:4-80) with the exact adjoints of this library's
+ * forward, computed deterministically (no atomics): weight gradients on the tensor cores
+ * (a GEMM over pixels), input gradients through the forward kernels with transposed weights.
+ * dtype BF16/F16, NHWC maps; weight and bias gradients are fp32; any output pointer may be
+ * NULL to skip that gradient.  Scratch is allocated stream-ordered on `stream`. */
+/* grad_x [N][H][W][Cin] = grad_out . w; grad_w [256][Cin] = sum_p grad_out^T x;
+ * grad_b [256] = sum_p grad_out.  w is the packed lateral weight [256][Cin] in dtype. */
+int ufpn_lateral_conv_backward(int dtype, const void* x, const void* w, const void* grad_out,
+                               void* grad_x, float* grad_w, float* grad_b, int N, int Cin, int H,
+                               int W, void* stream);
+/* 3x3 pad-1 conv 256 -> 256: grad_x = conv3x3(grad_out, w flipped and transposed);
+ * grad_w [256][9][256] (packed order: output channel, tap, input channel); grad_b [256].
+ * w is the packed weight [256][9][256] (ufpn_pack_conv3x3_weights). */
+int ufpn_conv3x3_backward(int dtype, const void* x, const void* w, const void* grad_out,
+                          void* grad_x, float* grad_w, float* grad_b, int N, int H, int W,
+                          void* stream);
+/* Top-down add: grad_coarse = base (or 0) + bilinear^T(grad_out) [N][Hc][Wc][C] (the lateral's
+ * gradient is grad_out itself). */
+int ufpn_upsample_add_backward(int dtype, const void* grad_out, const void* base,
+                               void* grad_coarse, int N, int C, int Hc, int Wc, int H, int W,
+                               void* stream);
+/* P6 = P5[::2, ::2]: grad_p5 at even pixels += grad_p6 (in place). */
+int ufpn_p6_backward(int dtype, const void* grad_p6, void* grad_p5, int N, int C, int H5, int W5,
+                     void* stream);
+
 /* P6 = max_pool2d(P5, kernel 1, stride 2).  No reference counterpart (the reference never
  * produces P6 although it takes C6, python/fpn_pytorch.cpp:84-86). */
 int ufpn_p6_maxpool(int dtype, int layout, const void* p5, void* p6, int N, int C, int H, int W,

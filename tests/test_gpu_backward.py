@@ -1,0 +1,149 @@
+"""Backward pass (training) on the GPU against autograd through the CPU oracle.
+
+The oracle's forward is the restated neck (oracle/fpn_oracle.py: conv2d laterals, the
+bilinear whose formula is pinned to the reference's upsample tests, pad-1 3x3, P6 = P5[::2,
+::2]); torch autograd through it gives the exact adjoints the library's backward kernels
+compute.  Inputs and weights are rounded to the kernels' 16-bit dtype first and the oracle
+runs in fp32, so the comparison measures the kernels' own rounding (16-bit gradient maps,
+fp32 accumulation)."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle import fpn_oracle as O
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2  # max |y - ref| / max |ref|, per tensor
+
+
+def _cl(x):
+    return x.contiguous(memory_format=torch.channels_last)
+
+
+def _rel(y, ref):
+    return O.rel_err(y.detach().float().cpu(), ref.detach().float())
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", [(2, 256, 20, 30), (1, 512, 25, 42), (1, 128, 33, 40), (2, 2048, 5, 7)])
+def test_lateral_conv_backward(cuda_device, dtype, shape):
+    import unified_fpn as U
+    n, cin, h, w = shape
+    g = torch.Generator().manual_seed(cin + h)
+    x = torch.randn(n, cin, h, w, generator=g).to(dtype)
+    wt = (torch.randn(256, cin, generator=g) * (2.0 / cin) ** 0.5).to(dtype)
+    gy = torch.randn(n, 256, h, w, generator=g).to(dtype)
+    gx, gw, gb = U.fpn_lateral_conv_backward(_cl(x.to(cuda_device)), wt.to(cuda_device), _cl(gy.to(cuda_device)))
+    torch.cuda.synchronize()
+    assert U.device_status() == 0
+    xr = x.float().requires_grad_()
+    wr = wt.float().requires_grad_()
+    br = torch.zeros(256, requires_grad=True)
+    O.lateral_conv(xr, wr, br).backward(gy.float())
+    assert _rel(gx, xr.grad) < TOL
+    assert _rel(gw, wr.grad) < TOL
+    assert _rel(gb, br.grad) < TOL
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", [(2, 20, 30), (1, 13, 17), (1, 50, 76)])
+def test_conv3x3_backward(cuda_device, dtype, shape):
+    import unified_fpn as U
+    n, h, w = shape
+    g = torch.Generator().manual_seed(h * 31 + w)
+    x = torch.randn(n, 256, h, w, generator=g).to(dtype)
+    w3 = (torch.randn(256, 256, 3, 3, generator=g) * 0.03).to(dtype)
+    gy = torch.randn(n, 256, h, w, generator=g).to(dtype)
+    gx, gw, gb = U.fpn_conv3x3_backward(_cl(x.to(cuda_device)), w3.to(cuda_device), _cl(gy.to(cuda_device)))
+    torch.cuda.synchronize()
+    assert U.device_status() == 0
+    xr = x.float().requires_grad_()
+    wr = w3.float().requires_grad_()
+    br = torch.zeros(256, requires_grad=True)
+    O.conv3x3(xr, wr, br).backward(gy.float())
+    assert _rel(gx, xr.grad) < TOL
+    assert _rel(gw, wr.grad) < TOL
+    assert _rel(gb, br.grad) < TOL
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("sizes", [((2, 256, 25, 38), (50, 76)), ((1, 256, 84, 50), (167, 100)),
+                                   ((1, 64, 7, 9), (13, 18)), ((1, 32, 5, 5), (5, 5))])
+def test_upsample_add_backward(cuda_device, dtype, sizes):
+    import unified_fpn as U
+    (n, c, hc, wc), (h, w) = sizes
+    g = torch.Generator().manual_seed(hc * 7 + wc)
+    gy = torch.randn(n, c, h, w, generator=g).to(dtype)
+    base = torch.randn(n, c, hc, wc, generator=g).to(dtype)
+    gc = U.fpn_upsample_add_backward(_cl(gy.to(cuda_device)), (hc, wc), base=_cl(base.to(cuda_device)))
+    cr = torch.zeros(n, c, hc, wc, requires_grad=True)
+    O.bilinear_upsample_t(cr, (h, w)).backward(gy.float())
+    ref = cr.grad + base.float()
+    assert _rel(gc, ref) < (1e-5 if dtype == torch.float32 else TOL)
+
+
+def test_p6_backward(cuda_device):
+    import unified_fpn as U
+    g = torch.Generator().manual_seed(3)
+    g5 = torch.randn(2, 256, 25, 38, generator=g).to(torch.bfloat16)
+    g6 = torch.randn(2, 256, 13, 19, generator=g).to(torch.bfloat16)
+    out = U.fpn_p6_backward(_cl(g6.to(cuda_device)), _cl(g5.to(cuda_device)))
+    ref = g5.float().clone()
+    ref[:, :, ::2, ::2] += g6.float()
+    assert torch.equal(out.cpu().float(), ref.to(torch.bfloat16).float())
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_neck_backward_matches_autograd(cuda_device, dtype):
+    """Every input, weight and bias gradient of the whole neck (R50 channels, 128x160 image,
+    batch 2, P6 included) against autograd through the oracle neck."""
+    import unified_fpn as U
+    sizes = O.level_sizes(128, 160)
+    fs = O.make_features(2, O.R50_CHANNELS, sizes, seed=21, dist="normal")
+    wts = O.make_weights(O.R50_CHANNELS, seed=22, bias_scale=0.1)
+    neck = U.FPNNeck(O.R50_CHANNELS).to(cuda_device)
+    with torch.no_grad():
+        for l in range(4):  # the module's fp32 master weights = the oracle's, rounded to dtype
+            neck.lateral_w[l].copy_(wts.lat_w[l].to(dtype).float())
+            neck.lateral_b[l].copy_(wts.lat_b[l])
+            neck.output_w[l].copy_(wts.out_w[l].to(dtype).float())
+            neck.output_b[l].copy_(wts.out_b[l])
+    feats = [_cl(f.to(dtype).to(cuda_device)).requires_grad_() for f in fs]
+    outs = neck(feats)
+    g = torch.Generator().manual_seed(23)
+    grads = [torch.randn(o.shape, generator=g).to(dtype) for o in outs]
+    torch.autograd.backward(outs, [_cl(gg.to(cuda_device)) for gg in grads])
+    torch.cuda.synchronize()
+    assert U.device_status() == 0
+
+    feats_r = [f.to(dtype).float().requires_grad_() for f in fs]
+    lw = [w.to(dtype).float().requires_grad_() for w in wts.lat_w]
+    lb = [b.clone().requires_grad_() for b in wts.lat_b]
+    ow = [w.to(dtype).float().requires_grad_() for w in wts.out_w]
+    ob = [b.clone().requires_grad_() for b in wts.out_b]
+    outs_r = O.fpn_neck(feats_r, O.NeckWeights(lw, lb, ow, ob))  # P2..P6
+    torch.autograd.backward(outs_r, [gg.float() for gg in grads])
+    for o, r in zip(outs, outs_r):  # the forward agrees first
+        assert _rel(o, r) < TOL
+    for f, r in zip(feats, feats_r):
+        assert _rel(f.grad, r.grad) < TOL
+    for l in range(4):
+        assert _rel(neck.lateral_w[l].grad, lw[l].grad) < TOL
+        assert _rel(neck.lateral_b[l].grad, lb[l].grad) < TOL
+        assert _rel(neck.output_w[l].grad, ow[l].grad) < TOL
+        assert _rel(neck.output_b[l].grad, ob[l].grad) < TOL
+
+
+def test_backward_is_deterministic(cuda_device):
+    """No atomics: two backward passes give bitwise the same gradients."""
+    import unified_fpn as U
+    g = torch.Generator().manual_seed(5)
+    x = _cl(torch.randn(2, 256, 40, 56, generator=g).to(torch.bfloat16).to(cuda_device))
+    w3 = (torch.randn(256, 256, 3, 3, generator=g) * 0.03).to(cuda_device)
+    gy = _cl(torch.randn(2, 256, 40, 56, generator=g).to(torch.bfloat16).to(cuda_device))
+    a = U.fpn_conv3x3_backward(x, w3, gy)
+    b = U.fpn_conv3x3_backward(x, w3, gy)
+    for p, q in zip(a, b):
+        assert torch.equal(p, q)
+    up = [U.fpn_upsample_add_backward(gy, (20, 28)) for _ in range(2)]
+    assert torch.equal(up[0], up[1])
