@@ -9,8 +9,9 @@
 // library's forward, computed deterministically:
 //
 //   * weight gradients, dW[o][tap][c] = sum_p dY[p][o] X[p + tap][c] (1x1: one tap; 3x3: the
-//     nine taps of pad-1), are a tensor-core GEMM over pixels: fpn_dw_gemm_kernel, M = 128
-//     output channels x N = 256 input channels per CTA, K = 64-pixel k-blocks fetched by TMA
+//     nine taps of pad-1), are a tensor-core GEMM over pixels: fpn_dw_gemm_kernel, all 256
+//     output channels (two M = 128 accumulators filling TMEM) x N = 256 input channels per CTA,
+//     K = 64-pixel k-blocks fetched by TMA
 //     as (64 channels x 64 pixels) boxes of the NHWC maps -- for both operands the channels
 //     are contiguous, i.e. MN-major operands, read through MN-major 128-byte-swizzle
 //     descriptors; the 3x3 taps shift the X box (TMA zero-fills outside the image = pad 1).
@@ -33,9 +34,9 @@ namespace ufpn {
 namespace {
 
 // ------------------------------------------------------------------ weight gradient GEMM
-constexpr int kDwStages = 4;
+constexpr int kDwStages = 3;
 constexpr int kDwChunk = 64 * 128;         // one 64-channel x 64-pixel box, 16-bit: 8 KB
-constexpr int kDwAStage = 2 * kDwChunk;    // 128 output channels
+constexpr int kDwAStage = 4 * kDwChunk;    // 256 output channels (two M = 128 operands)
 constexpr int kDwBStage = 4 * kDwChunk;    // 256 input channels
 constexpr int kDwOffB = kDwStages * kDwAStage;
 constexpr int kDwOffBars = kDwOffB + kDwStages * kDwBStage;
@@ -72,14 +73,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  // work unit: (tap, 128-channel output block, 256-channel input block, pixel split)
+  // work unit: (tap, 256-channel input block, pixel split); every unit covers all 256 outputs
   int r = static_cast<int>(blockIdx.x);
   const int split = r % a.ksplit;
   r /= a.ksplit;
   const int cb = r % a.c_blocks;
-  r /= a.c_blocks;
-  const int ob = r % 2;
-  const int tap = r / 2;
+  const int tap = r / a.c_blocks;
   const int dy = a.taps == 9 ? tap / 3 - 1 : 0;
   const int dx = a.taps == 9 ? tap % 3 - 1 : 0;
   const int kb0 = split * a.per_kb;
@@ -98,7 +97,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     prefetch_tmap(&map_x);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kTcBlockN);
+    tmem_alloc(tmem_slot, 2 * kTcBlockN);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -119,9 +118,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int n = t2 / a.tiles_y;
         const int x0 = tx * a.kw, y0 = ty * a.kh;
         mbar_arrive_expect_tx(&full_bar[stage], kDwAStage + kDwBStage);
-        for (int j = 0; j < 2; ++j)
+        for (int j = 0; j < 4; ++j)
           tma_load_4d(smem_a + stage * kDwAStage + j * kDwChunk, &map_g, &full_bar[stage],
-                      ob * 128 + j * 64, x0, y0, n, kPolicyEvictFirst);
+                      j * 64, x0, y0, n, kPolicyEvictFirst);
         for (int j = 0; j < 4; ++j)
           tma_load_4d(smem_b + stage * kDwBStage + j * kDwChunk, &map_x, &full_bar[stage],
                       cb * 256 + j * 64, x0 + dx, y0 + dy, n, kPolicyEvictFirst);
@@ -154,12 +153,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint64_t adesc = sdesc_mnmajor_sw128(smem_u32(smem_a + stage * kDwAStage), kDwChunk);
+        // A: output channels 0..127 (chunks 0, 1) and 128..255 (chunks 2, 3), one accumulator each
+        const uint32_t a_addr = smem_u32(smem_a + stage * kDwAStage);
+        const uint64_t adesc0 = sdesc_mnmajor_sw128(a_addr, kDwChunk);
+        const uint64_t adesc1 = sdesc_mnmajor_sw128(a_addr + 2 * kDwChunk, kDwChunk);
         const uint64_t bdesc = sdesc_mnmajor_sw128(smem_u32(smem_b + stage * kDwBStage), kDwChunk);
 #pragma unroll
-        for (int k = 0; k < kMmaPerKb; ++k)  // +16 pixel rows (2048 bytes) per MMA step
-          tc_mma<T>(tmem_base, adesc + 128u * k, bdesc + 128u * k, idesc,
-                    (kb > kb0 || k > 0) ? 1u : 0u);
+        for (int k = 0; k < kMmaPerKb; ++k) {  // +16 pixel rows (2048 bytes) per MMA step
+          const uint32_t acc = (kb > kb0 || k > 0) ? 1u : 0u;
+          tc_mma<T>(tmem_base, adesc0 + 128u * k, bdesc + 128u * k, idesc, acc);
+          tc_mma<T>(tmem_base + kTcBlockN, adesc1 + 128u * k, bdesc + 128u * k, idesc, acc);
+        }
         tc_commit(&empty_bar[stage]);
         if (++stage == S) {
           stage = 0;
@@ -171,20 +175,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_wait_drain(done_bar, 0);
     }
   } else {
-    // epilogue: TMEM lane = output channel o, column = input channel c; fp32 partial rows
+    // epilogue: accumulator `half` (output channels half*128..), TMEM lane = output channel,
+    // column = input channel; fp32 partial rows
     const int quarter = warp & 3;
-    const int chalf = (warp - 2) >> 2;
-    const int o = ob * 128 + quarter * 32 + lane;
+    const int half = (warp - 2) >> 2;
+    const int o = half * 128 + quarter * 32 + lane;
     const bool ok = mbar_wait(accf_bar, 0, abort_flag, a.status, kDevTimeoutDw);
     if (__all_sync(0xffffffffu, ok)) {
       tc_fence_after();
       float* row = a.partial +
                    ((static_cast<size_t>(split) * a.taps + tap) * 256 + o) * a.Cin;
 #pragma unroll 1
-      for (int h = 0; h < 4; ++h) {
-        const int col = chalf * 128 + h * 32;
+      for (int h = 0; h < 8; ++h) {
+        const int col = h * 32;
         uint32_t v[32];
-        tmem_ld32(tmem_base + static_cast<uint32_t>(col) + (static_cast<uint32_t>(quarter * 32) << 16),
+        tmem_ld32(tmem_base + static_cast<uint32_t>(half * kTcBlockN + col) +
+                      (static_cast<uint32_t>(quarter * 32) << 16),
                   v);
         tmem_wait_ld();
         const int c0 = cb * 256 + col;
@@ -208,19 +214,31 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTcBlockN);
+    tmem_dealloc(tmem_base, 2 * kTcBlockN);
   }
 }
 
-// out[(o * taps + t) * Cin + c] = sum over s (in order) of partial[s][t][o][c]
+// out[(o * taps + t) * Cin + c] = sum over s of partial[s][t][o][c], in a fixed order: four
+// running sums over s = 0, 4, 8, .. / 1, 5, 9, .. / .., added last (four loads in flight per
+// thread instead of one dependent chain of ksplit loads)
 __global__ void __launch_bounds__(256) reduce_partials_kernel(const float* __restrict__ partial,
                                                               float* __restrict__ out, int ksplit,
                                                               int taps, int Cin) {
   const long long per = static_cast<long long>(taps) * 256 * Cin;
   for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < per;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    float acc = 0.f;
-    for (int s = 0; s < ksplit; ++s) acc += partial[s * per + i];
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    int s = 0;
+    for (; s + 4 <= ksplit; s += 4) {
+      a0 += __ldg(partial + s * per + i);
+      a1 += __ldg(partial + (s + 1) * per + i);
+      a2 += __ldg(partial + (s + 2) * per + i);
+      a3 += __ldg(partial + (s + 3) * per + i);
+    }
+    if (s < ksplit) a0 += __ldg(partial + s * per + i);
+    if (s + 1 < ksplit) a1 += __ldg(partial + (s + 1) * per + i);
+    if (s + 2 < ksplit) a2 += __ldg(partial + (s + 2) * per + i);
+    const float acc = (a0 + a1) + (a2 + a3);
     const int c = static_cast<int>(i % Cin);
     const long long to = i / Cin;
     const int o = static_cast<int>(to % 256);
@@ -257,15 +275,56 @@ __device__ __forceinline__ __nv_bfloat16 bw_from_f<__nv_bfloat16>(float v) {
   return __float2bfloat16_rn(v);
 }
 
-// part[b][c] = sum of g[p][c] over the pixels p of block b's contiguous run (thread = channel)
+// part[b][c] = sum of g[p][c] over block b's contiguous run of pixels.  vt = C * sizeof(T) / 16
+// threads cover a pixel's 16-byte vectors; the block's 256 / vt pixel lanes run through its
+// pixels with that stride, two loads in flight each; the lanes' sums are then added in lane
+// order (fixed: the result does not depend on timing).
 template <typename T>
 __global__ void __launch_bounds__(256) colsum_kernel(const T* __restrict__ g, long long pixels,
                                                      int C, long long per, float* __restrict__ part) {
+  constexpr int V = 16 / sizeof(T);
+  __shared__ float red[256 * V];
+  const int vt = C / V;
+  const int lanes = 256 / vt;
+  const int cv = threadIdx.x % vt;   // 16-byte vector: channels cv*V .. +V-1
+  const int pl = threadIdx.x / vt;   // pixel lane
   const long long p0 = static_cast<long long>(blockIdx.x) * per;
   const long long p1 = min(pixels, p0 + per);
+  float a[V], b[V];
+#pragma unroll
+  for (int e = 0; e < V; ++e) a[e] = b[e] = 0.f;
+  const bool active = pl < lanes;
+  long long p = p0 + pl;
+  for (; active && p + lanes < p1; p += 2 * lanes) {
+    union {
+      uint4 u;
+      T e[V];
+    } x, y;
+    x.u = __ldg(reinterpret_cast<const uint4*>(g + p * C) + cv);
+    y.u = __ldg(reinterpret_cast<const uint4*>(g + (p + lanes) * C) + cv);
+#pragma unroll
+    for (int e = 0; e < V; ++e) {
+      a[e] += bw_to_f(x.e[e]);
+      b[e] += bw_to_f(y.e[e]);
+    }
+  }
+  if (active && p < p1) {
+    union {
+      uint4 u;
+      T e[V];
+    } x;
+    x.u = __ldg(reinterpret_cast<const uint4*>(g + p * C) + cv);
+#pragma unroll
+    for (int e = 0; e < V; ++e) a[e] += bw_to_f(x.e[e]);
+  }
+  if (active) {
+#pragma unroll
+    for (int e = 0; e < V; ++e) red[pl * C + cv * V + e] = a[e] + b[e];
+  }
+  __syncthreads();
   for (int c = threadIdx.x; c < C; c += blockDim.x) {
     float acc = 0.f;
-    for (long long p = p0; p < p1; ++p) acc += bw_to_f(g[p * C + c]);
+    for (int l = 0; l < lanes; ++l) acc += red[l * C + c];
     part[static_cast<size_t>(blockIdx.x) * C + c] = acc;
   }
 }
@@ -427,6 +486,17 @@ void dw_block_shape(int H, int W, int& kw, int& kh) {
   }
 }
 
+// Pixel split of the weight-gradient GEMM: about one wave of CTAs over all units (taps x
+// input-channel blocks), at least 4 k-blocks per split, every split non-empty.
+void dw_split(int num_kb, int units, int& per, int& ksplit) {
+  int k = sm_count() / units;
+  if (k < 1) k = 1;
+  const int cap = num_kb / 4 > 0 ? num_kb / 4 : 1;
+  if (k > cap) k = cap;
+  per = (num_kb + k - 1) / k;
+  ksplit = (num_kb + per - 1) / per;
+}
+
 int grid_for(long long work, int block) {
   const long long g = (work + block - 1) / block;
   return static_cast<int>(g < 148LL * 32 ? (g > 0 ? g : 1) : 148LL * 32);
@@ -439,13 +509,9 @@ size_t dw_gemm_workspace_bytes(int N, int H, int W, int Cin, int taps) {
   int kw = 64, kh = 1;
   dw_block_shape(H, W, kw, kh);
   const int num_kb = ((W + kw - 1) / kw) * ((H + kh - 1) / kh) * N;
-  const int c_blocks = (Cin + 255) / 256;
-  const int units = taps * 2 * c_blocks;
-  // pixel splits: about two CTAs per SM over all units, at least 4 k-blocks per split
-  int ksplit = (2 * sm_count() + units - 1) / units;
-  ksplit = ksplit < num_kb / 4 ? ksplit : (num_kb / 4 > 0 ? num_kb / 4 : 1);
-  const int per = (num_kb + ksplit - 1) / ksplit;
-  ksplit = (num_kb + per - 1) / per;
+  const int units = taps * ((Cin + 255) / 256);
+  int per = 1, ksplit = 1;
+  dw_split(num_kb, units, per, ksplit);
   return static_cast<size_t>(ksplit) * taps * 256 * Cin * sizeof(float);
 }
 
@@ -466,11 +532,8 @@ cudaError_t launch_dw_gemm(DType dt, const void* grad_out, const void* x, int N,
   a.c_blocks = (Cin + 255) / 256;
   a.taps = taps;
   a.Cin = Cin;
-  const int units = taps * 2 * a.c_blocks;
-  int ksplit = (2 * sm_count() + units - 1) / units;
-  ksplit = ksplit < a.num_kb / 4 ? ksplit : (a.num_kb / 4 > 0 ? a.num_kb / 4 : 1);
-  a.per_kb = (a.num_kb + ksplit - 1) / ksplit;
-  a.ksplit = (a.num_kb + a.per_kb - 1) / a.per_kb;  // every split non-empty
+  const int units = taps * a.c_blocks;
+  dw_split(a.num_kb, units, a.per_kb, a.ksplit);
   a.partial = workspace;
   a.status = status;
   if (static_cast<size_t>(a.ksplit) * taps * 256 * Cin * sizeof(float) > ws_bytes)
@@ -507,6 +570,9 @@ size_t colsum_workspace_bytes(long long pixels, int C) {
 cudaError_t launch_colsum(DType dt, const void* g, long long pixels, int C, float* out,
                           float* workspace, size_t ws_bytes, cudaStream_t s) {
   if (pixels <= 0 || C <= 0 || !g || !out || !workspace) return cudaErrorInvalidValue;
+  // 16-byte vectors, at most one per thread, cover a pixel's channels
+  if ((C * dtype_size(dt)) % 16 != 0 || C * dtype_size(dt) > 256 * 16 || !aligned16(g))
+    return cudaErrorNotSupported;
   const long long blocks = pixels < 1024 ? pixels : 1024;
   const long long per = (pixels + blocks - 1) / blocks;
   const int nb = static_cast<int>((pixels + per - 1) / per);

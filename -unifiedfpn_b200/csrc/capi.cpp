@@ -428,12 +428,27 @@ int ufpn_merge_two_levels(int dtype, const void* m5, const void* l4, void* m4, v
 }
 
 namespace {
-// Stream-ordered scratch for one backward call, freed (stream-ordered) on scope exit.
+// Stream-ordered scratch for one backward call, freed (stream-ordered) on scope exit.  The
+// device's default pool keeps freed memory cached (release threshold raised once per device),
+// so repeated calls reuse it instead of mapping and unmapping tens of MB every time.
 struct StreamScratch {
   cudaStream_t s;
   void* p = nullptr;
   explicit StreamScratch(cudaStream_t st) : s(st) {}
-  cudaError_t alloc(size_t bytes) { return cudaMallocAsync(&p, bytes > 0 ? bytes : 16, s); }
+  cudaError_t alloc(size_t bytes) {
+    static bool cached[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !cached[dev]) {
+      cudaMemPool_t pool;
+      if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
+        uint64_t keep = UINT64_MAX;
+        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+      }
+      cached[dev] = true;
+    }
+    return cudaMallocAsync(&p, bytes > 0 ? bytes : 16, s);
+  }
   ~StreamScratch() {
     if (p) cudaFreeAsync(p, s);
   }
