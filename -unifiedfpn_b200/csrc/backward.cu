@@ -27,6 +27,9 @@
 #include "kernels.h"
 #include "tc_gemm.cuh"
 
+#include <algorithm>
+#include <atomic>
+#include <cmath>
 #include <cstring>
 
 namespace ufpn {
@@ -277,7 +280,7 @@ __device__ __forceinline__ __nv_bfloat16 bw_from_f<__nv_bfloat16>(float v) {
 
 // part[b][c] = sum of g[p][c] over block b's contiguous run of pixels.  vt = C * sizeof(T) / 16
 // threads cover a pixel's 16-byte vectors; the block's 256 / vt pixel lanes run through its
-// pixels with that stride, two loads in flight each; the lanes' sums are then added in lane
+// pixels with that stride, four loads in flight each; the lanes' sums are then added in lane
 // order (fixed: the result does not depend on timing).
 template <typename T>
 __global__ void __launch_bounds__(256) colsum_kernel(const T* __restrict__ g, long long pixels,
@@ -290,36 +293,38 @@ __global__ void __launch_bounds__(256) colsum_kernel(const T* __restrict__ g, lo
   const int pl = threadIdx.x / vt;   // pixel lane
   const long long p0 = static_cast<long long>(blockIdx.x) * per;
   const long long p1 = min(pixels, p0 + per);
-  float a[V], b[V];
+  float a[4][V];
 #pragma unroll
-  for (int e = 0; e < V; ++e) a[e] = b[e] = 0.f;
+  for (int q = 0; q < 4; ++q)
+#pragma unroll
+    for (int e = 0; e < V; ++e) a[q][e] = 0.f;
   const bool active = pl < lanes;
   long long p = p0 + pl;
-  for (; active && p + lanes < p1; p += 2 * lanes) {
+  for (; active && p + 3 * lanes < p1; p += 4 * lanes) {
     union {
       uint4 u;
       T e[V];
-    } x, y;
-    x.u = __ldg(reinterpret_cast<const uint4*>(g + p * C) + cv);
-    y.u = __ldg(reinterpret_cast<const uint4*>(g + (p + lanes) * C) + cv);
+    } x[4];
 #pragma unroll
-    for (int e = 0; e < V; ++e) {
-      a[e] += bw_to_f(x.e[e]);
-      b[e] += bw_to_f(y.e[e]);
-    }
+    for (int q = 0; q < 4; ++q)
+      x[q].u = __ldg(reinterpret_cast<const uint4*>(g + (p + q * lanes) * C) + cv);
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+#pragma unroll
+      for (int e = 0; e < V; ++e) a[q][e] += bw_to_f(x[q].e[e]);
   }
-  if (active && p < p1) {
+  for (; active && p < p1; p += lanes) {
     union {
       uint4 u;
       T e[V];
     } x;
     x.u = __ldg(reinterpret_cast<const uint4*>(g + p * C) + cv);
 #pragma unroll
-    for (int e = 0; e < V; ++e) a[e] += bw_to_f(x.e[e]);
+    for (int e = 0; e < V; ++e) a[0][e] += bw_to_f(x.e[e]);
   }
   if (active) {
 #pragma unroll
-    for (int e = 0; e < V; ++e) red[pl * C + cv * V + e] = a[e] + b[e];
+    for (int e = 0; e < V; ++e) red[pl * C + cv * V + e] = (a[0][e] + a[1][e]) + (a[2][e] + a[3][e]);
   }
   __syncthreads();
   for (int c = threadIdx.x; c < C; c += blockDim.x) {
@@ -328,13 +333,29 @@ __global__ void __launch_bounds__(256) colsum_kernel(const T* __restrict__ g, lo
     part[static_cast<size_t>(blockIdx.x) * C + c] = acc;
   }
 }
-__global__ void __launch_bounds__(256) sum_rows_kernel(const float* __restrict__ part, int rows,
-                                                       int C, float* __restrict__ out) {
-  const int c = static_cast<int>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (c >= C) return;
-  float acc = 0.f;
-  for (int r = 0; r < rows; ++r) acc += part[static_cast<size_t>(r) * C + c];
-  out[c] = acc;
+// out[c] = sum over r of part[r][c]: a block takes 32 channels, its 32 row lanes sum every
+// 32nd row (four running sums each) and the lanes' sums are added in lane order (fixed order).
+__global__ void __launch_bounds__(1024) sum_rows_kernel(const float* __restrict__ part, int rows,
+                                                        int C, float* __restrict__ out) {
+  __shared__ float red[32][33];
+  const int cl = threadIdx.x & 31, lane = threadIdx.x >> 5;
+  const int c = static_cast<int>(blockIdx.x) * 32 + cl;
+  float a[4] = {0.f, 0.f, 0.f, 0.f};
+  if (c < C) {
+    int r = lane;
+    for (; r + 96 < rows; r += 128) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) a[q] += part[static_cast<size_t>(r + 32 * q) * C + c];
+    }
+    for (; r < rows; r += 32) a[0] += part[static_cast<size_t>(r) * C + c];
+  }
+  red[lane][cl] = (a[0] + a[1]) + (a[2] + a[3]);
+  __syncthreads();
+  if (lane == 0 && c < C) {
+    float acc = 0.f;
+    for (int l = 0; l < 32; ++l) acc += red[l][cl];
+    out[c] = acc;
+  }
 }
 
 // ------------------------------------------------------------------ top-down adjoint
@@ -414,6 +435,223 @@ __global__ void __launch_bounds__(256) upsample_adjoint_kernel(
       for (int e = 0; e < V; ++e) o.e[e] = bw_from_f<T>(acc[e]);
     }
     *(reinterpret_cast<uint4*>(out + ob) + cv) = o.u;
+  }
+}
+
+// fine rows (columns) whose taps can reach coarse row (column) q: [tap_lo, tap_hi], a superset
+// of the nonzero ones (weights decide); the clamped tail of the last coarse index reaches the end
+__device__ __forceinline__ int tap_lo(int q, float inv) {
+  return max(0, static_cast<int>(floorf((q - 1 + 0.5f) * inv - 0.5f)) - 1);
+}
+__device__ __forceinline__ int tap_hi(int q, int in, int out, float inv) {
+  return q == in - 1 ? out - 1 : min(out - 1, static_cast<int>(ceilf((q + 1 + 0.5f) * inv - 0.5f)) + 1);
+}
+
+constexpr int kUaTapsMax = 24;  // fine rows (columns) with a nonzero weight per coarse one
+constexpr int kUaStripMax = 16;  // coarse columns per block
+constexpr int kUaThreads = 256;
+
+// 16 bytes of T <-> V floats with packed conversions (bf16: a shift or a mask per element)
+template <typename T>
+struct Vec16;
+template <>
+struct Vec16<__nv_bfloat16> {
+  static constexpr int V = 8;
+  static __device__ __forceinline__ void unpack(const uint4& u, float (&f)[8]) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[2 * i] = __uint_as_float(w[i] << 16);
+      f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  }
+  static __device__ __forceinline__ uint4 pack(const float (&f)[8]) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+      w[i] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+  }
+};
+template <>
+struct Vec16<__half> {
+  static constexpr int V = 8;
+  static __device__ __forceinline__ void unpack(const uint4& u, float (&f)[8]) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+      f[2 * i] = t.x;
+      f[2 * i + 1] = t.y;
+    }
+  }
+  static __device__ __forceinline__ uint4 pack(const float (&f)[8]) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __half2 h = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+      w[i] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+  }
+};
+template <>
+struct Vec16<float> {
+  static constexpr int V = 4;
+  static __device__ __forceinline__ void unpack(const uint4& u, float (&f)[4]) {
+    f[0] = __uint_as_float(u.x);
+    f[1] = __uint_as_float(u.y);
+    f[2] = __uint_as_float(u.z);
+    f[3] = __uint_as_float(u.w);
+  }
+  static __device__ __forceinline__ uint4 pack(const float (&f)[4]) {
+    return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
+                      __float_as_uint(f[3]));
+  }
+};
+
+// acc += w * (16 bytes of T)
+template <typename T, int V>
+__device__ __forceinline__ void fma_vec(float (&acc)[V], const uint4& u, float w) {
+  float f[V];
+  Vec16<T>::unpack(u, f);
+#pragma unroll
+  for (int e = 0; e < V; ++e) acc[e] = fmaf(f[e], w, acc[e]);
+}
+
+// Same sum as upsample_adjoint_kernel, separably: a block takes coarse row yc of image n and a
+// strip of up to TX coarse columns.  The fine rows that reach yc and the fine columns that reach
+// each coarse column of the strip are listed once, with their weights, in shared memory (the
+// scale is at most 8, so at most 2 * 8 + 1 of either have a nonzero weight).  Pass 1 sums the
+// listed fine rows, weighted, into fp32 rows of shared memory, one per fine column the strip
+// reaches (16-byte vectors; a thread keeps its vector and steps over fine columns, loads of
+// four rows issued before their math, the first four rows' offsets and weights held in
+// registers); pass 2 forms each coarse pixel of the strip from its listed fine columns there and
+// adds `base`.  Each fine pixel is read once per coarse row it reaches (about twice at scale 2),
+// not once per coarse pixel (four times).  In shared memory the four-float quarter q of channel
+// vector cv of fine column j sits at j * C + (q * C / V + cv) * 4: a warp's 16-byte accesses are
+// contiguous.  C / V <= 256.
+template <typename T>
+__global__ void __launch_bounds__(kUaThreads) upsample_adjoint_staged_kernel(
+    const T* __restrict__ g, const T* base, T* out, int C, int Hc, int Wc, int H, int W, float sy,
+    float sx, int TX) {
+  constexpr int V = Vec16<T>::V;
+  constexpr int Q = V / 4;  // float4 quarters per vector
+  extern __shared__ float4 ua_smem[];
+  float* R = reinterpret_cast<float*>(ua_smem);  // [span][C]
+  __shared__ long long row_off[kUaTapsMax];      // element offset of the fine row in the image
+  __shared__ float row_w[kUaTapsMax];
+  __shared__ int nrows;
+  __shared__ short col_x[kUaStripMax][kUaTapsMax];  // fine column - fx0
+  __shared__ float col_w[kUaStripMax][kUaTapsMax];
+  __shared__ int ncols[kUaStripMax];
+  const int strips = (Wc + TX - 1) / TX;
+  const int strip = static_cast<int>(blockIdx.x % strips);
+  const int yc = static_cast<int>((blockIdx.x / strips) % Hc);
+  const int n = static_cast<int>(blockIdx.x / strips / Hc);
+  const int xc0 = strip * TX, xc1 = min(Wc, xc0 + TX) - 1;
+  const float iy = 1.f / sy, ix = 1.f / sx;
+  const int fx0 = tap_lo(xc0, ix);
+  const int span = tap_hi(xc1, Wc, W, ix) - fx0 + 1;
+  if (threadIdx.x == 0) {
+    int k = 0;
+    for (int y = tap_lo(yc, iy), ye = tap_hi(yc, Hc, H, iy); y <= ye; ++y) {
+      const float w = bw_tap_weight(y, yc, Hc, sy);
+      if (w != 0.f && k < kUaTapsMax) {
+        row_off[k] = static_cast<long long>(y) * W * C;
+        row_w[k] = w;
+        ++k;
+      }
+    }
+    nrows = k;
+  } else if (threadIdx.x >= 32 && threadIdx.x < 32 + xc1 - xc0 + 1) {
+    const int xl = threadIdx.x - 32, xc = xc0 + xl;
+    int k = 0;
+    for (int x = tap_lo(xc, ix), xe = tap_hi(xc, Wc, W, ix); x <= xe; ++x) {
+      const float w = bw_tap_weight(x, xc, Wc, sx);
+      if (w != 0.f && k < kUaTapsMax) {
+        col_x[xl][k] = static_cast<short>(x - fx0);
+        col_w[xl][k] = w;
+        ++k;
+      }
+    }
+    ncols[xl] = k;
+  }
+  const int cvn = C / V;
+  const int jstep = kUaThreads / cvn;  // fine columns in flight per block
+  const int cv = threadIdx.x % cvn, j0 = threadIdx.x / cvn;
+  __syncthreads();
+  const int nr = nrows;
+  long long ro[4];
+  float rwt[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    ro[q] = q < nr ? row_off[q] : 0;
+    rwt[q] = q < nr ? row_w[q] : 0.f;
+  }
+  const T* gn = g + static_cast<size_t>(n) * H * W * C + cv * V;
+  if (j0 < jstep) {
+    for (int j = j0; j < span; j += jstep) {
+      const T* src = gn + static_cast<size_t>(fx0 + j) * C;
+      float acc[V];
+#pragma unroll
+      for (int e = 0; e < V; ++e) acc[e] = 0.f;
+      uint4 v[4];
+      if (nr >= 4) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) v[q] = __ldg(reinterpret_cast<const uint4*>(src + ro[q]));
+#pragma unroll
+        for (int q = 0; q < 4; ++q) fma_vec<T, V>(acc, v[q], rwt[q]);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 3; ++q)
+          if (q < nr) v[q] = __ldg(reinterpret_cast<const uint4*>(src + ro[q]));
+#pragma unroll
+        for (int q = 0; q < 3; ++q)
+          if (q < nr) fma_vec<T, V>(acc, v[q], rwt[q]);
+      }
+      for (int r = 4; r < nr; r += 4) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (r + q < nr) v[q] = __ldg(reinterpret_cast<const uint4*>(src + row_off[r + q]));
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (r + q < nr) fma_vec<T, V>(acc, v[q], row_w[r + q]);
+      }
+      float4* dst = reinterpret_cast<float4*>(R + static_cast<size_t>(j) * C) + cv;
+#pragma unroll
+      for (int q = 0; q < Q; ++q)
+        dst[q * cvn] = make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
+    }
+  }
+  __syncthreads();
+  if (j0 >= jstep) return;
+  const size_t orow = (static_cast<size_t>(n) * Hc + yc) * Wc;
+  for (int xl = j0; xl <= xc1 - xc0; xl += jstep) {
+    float acc[V];
+#pragma unroll
+    for (int e = 0; e < V; ++e) acc[e] = 0.f;
+    const int nc = ncols[xl];
+    for (int k = 0; k < nc; ++k) {
+      const float w = col_w[xl][k];
+      const float4* r4 = reinterpret_cast<const float4*>(R + static_cast<size_t>(col_x[xl][k]) * C) + cv;
+#pragma unroll
+      for (int q = 0; q < Q; ++q) {
+        const float4 f = r4[q * cvn];
+        acc[4 * q] = fmaf(f.x, w, acc[4 * q]);
+        acc[4 * q + 1] = fmaf(f.y, w, acc[4 * q + 1]);
+        acc[4 * q + 2] = fmaf(f.z, w, acc[4 * q + 2]);
+        acc[4 * q + 3] = fmaf(f.w, w, acc[4 * q + 3]);
+      }
+    }
+    uint4* dst = reinterpret_cast<uint4*>(out + (orow + xc0 + xl) * C) + cv;
+    if (base) {
+      const uint4 b = *(reinterpret_cast<const uint4*>(base + (orow + xc0 + xl) * C) + cv);
+      fma_vec<T, V>(acc, b, 1.f);
+    }
+    *dst = Vec16<T>::pack(acc);
   }
 }
 
@@ -562,9 +800,16 @@ cudaError_t launch_dw_gemm(DType dt, const void* grad_out, const void* x, int N,
                    1, static_cast<const float*>(workspace), grad_w, a.ksplit, taps, Cin);
 }
 
+// Column sums: at most 4 blocks per SM (all resident at once), each over a contiguous run of at
+// least 64 pixels.
+static long long colsum_blocks(long long pixels) {
+  const long long cap = 4LL * sm_count();
+  const long long b = (pixels + 63) / 64;
+  return b < 1 ? 1 : (b < cap ? b : cap);
+}
+
 size_t colsum_workspace_bytes(long long pixels, int C) {
-  const long long blocks = pixels < 1024 ? (pixels > 0 ? pixels : 1) : 1024;
-  return static_cast<size_t>(blocks) * C * sizeof(float);
+  return static_cast<size_t>(colsum_blocks(pixels)) * C * sizeof(float);
 }
 
 cudaError_t launch_colsum(DType dt, const void* g, long long pixels, int C, float* out,
@@ -573,7 +818,7 @@ cudaError_t launch_colsum(DType dt, const void* g, long long pixels, int C, floa
   // 16-byte vectors, at most one per thread, cover a pixel's channels
   if ((C * dtype_size(dt)) % 16 != 0 || C * dtype_size(dt) > 256 * 16 || !aligned16(g))
     return cudaErrorNotSupported;
-  const long long blocks = pixels < 1024 ? pixels : 1024;
+  const long long blocks = colsum_blocks(pixels);
   const long long per = (pixels + blocks - 1) / blocks;
   const int nb = static_cast<int>((pixels + per - 1) / per);
   if (static_cast<size_t>(nb) * C * sizeof(float) > ws_bytes) return cudaErrorInvalidValue;
@@ -595,8 +840,24 @@ cudaError_t launch_colsum(DType dt, const void* g, long long pixels, int C, floa
       return cudaErrorNotSupported;
   }
   if (e != cudaSuccess) return e;
-  return launch_ex(sum_rows_kernel, dim3((C + 255) / 256), dim3(256), 0, s, LaunchOpts(), 1,
+  return launch_ex(sum_rows_kernel, dim3((C + 31) / 32), dim3(1024), 0, s, LaunchOpts(), 1,
                    static_cast<const float*>(workspace), nb, C, out);
+}
+
+template <typename K, typename... Args>
+cudaError_t launch_staged_adjoint(K kernel, long long blocks, size_t smem, cudaStream_t s,
+                                  Args... args) {
+  static std::atomic<bool> opted[64];  // per device: the attribute belongs to its context
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 64 || !opted[dev].load(std::memory_order_acquire)) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    if (e != cudaSuccess) return e;
+    if (dev < 64) opted[dev].store(true, std::memory_order_release);
+  }
+  return launch_ex(kernel, dim3(static_cast<unsigned>(blocks)), dim3(kUaThreads), smem, s,
+                   LaunchOpts(), 1, args...);
 }
 
 cudaError_t launch_upsample_adjoint(DType dt, const void* grad_fine, const void* base, void* out,
@@ -609,6 +870,40 @@ cudaError_t launch_upsample_adjoint(DType dt, const void* grad_fine, const void*
   const int esz = dtype_size(dt);
   if ((C * esz) % 16 != 0) return cudaErrorInvalidValue;
   const float sy = static_cast<float>(Hc) / H, sx = static_cast<float>(Wc) / W;  // forward scales
+  // Staged kernel: at most 8 fine rows / columns per coarse one (then at most 2 * 8 + 1 fine
+  // rows or columns have a nonzero weight for a coarse one: their source coordinate lies in an
+  // open interval of length 2), a strip of TX coarse columns whose fine span, bounded by
+  // (TX + 1) W / Wc + 6, fits the shared-memory rows, and one 16-byte vector per thread.
+  constexpr size_t kUaSmemMax = 160 * 1024;
+  const double ratio = static_cast<double>(W) / Wc;
+  auto span_bound = [&](int tx) { return static_cast<int>(std::ceil((tx + 1) * ratio)) + 6; };
+  int TX = std::min(kUaStripMax, Wc);
+  while (TX > 1 && static_cast<size_t>(span_bound(TX)) * C * 4 > 64 * 1024) --TX;
+  const size_t smem = static_cast<size_t>(span_bound(TX)) * C * 4;
+  const long long strips = (Wc + TX - 1) / TX;
+  const long long blocks = static_cast<long long>(N) * Hc * strips;
+  if (H <= 8 * Hc && W <= 8 * Wc && C / (16 / esz) <= kUaThreads && smem <= kUaSmemMax &&
+      span_bound(TX) < 32768 && blocks < (1LL << 31)) {
+    switch (dt) {
+      case DType::F32:
+        return launch_staged_adjoint(upsample_adjoint_staged_kernel<float>, blocks, smem, s,
+                                     static_cast<const float*>(grad_fine),
+                                     static_cast<const float*>(base), static_cast<float*>(out), C,
+                                     Hc, Wc, H, W, sy, sx, TX);
+      case DType::F16:
+        return launch_staged_adjoint(upsample_adjoint_staged_kernel<__half>, blocks, smem, s,
+                                     static_cast<const __half*>(grad_fine),
+                                     static_cast<const __half*>(base), static_cast<__half*>(out), C,
+                                     Hc, Wc, H, W, sy, sx, TX);
+      case DType::BF16:
+        return launch_staged_adjoint(upsample_adjoint_staged_kernel<__nv_bfloat16>, blocks, smem, s,
+                                     static_cast<const __nv_bfloat16*>(grad_fine),
+                                     static_cast<const __nv_bfloat16*>(base),
+                                     static_cast<__nv_bfloat16*>(out), C, Hc, Wc, H, W, sy, sx, TX);
+      default:
+        return cudaErrorNotSupported;
+    }
+  }
   const long long pixels = static_cast<long long>(N) * Hc * Wc;
   const dim3 grid(static_cast<unsigned>((pixels + 7) / 8));
   switch (dt) {

@@ -68,7 +68,9 @@ def test_conv3x3_backward(cuda_device, dtype, shape):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("sizes", [((2, 256, 25, 38), (50, 76)), ((1, 256, 84, 50), (167, 100)),
-                                   ((1, 64, 7, 9), (13, 18)), ((1, 32, 5, 5), (5, 5))])
+                                   ((1, 64, 7, 9), (13, 18)), ((1, 32, 5, 5), (5, 5)),
+                                   ((1, 1024, 6, 10), (12, 20)),   # wide rows: narrow strips
+                                   ((1, 32, 2, 3), (40, 50))])     # scale > 8: the gather kernel
 def test_upsample_add_backward(cuda_device, dtype, sizes):
     import unified_fpn as U
     (n, c, hc, wc), (h, w) = sizes
