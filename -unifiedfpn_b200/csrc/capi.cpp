@@ -475,7 +475,7 @@ int ufpn_lateral_conv_backward(int dtype, const void* x, const void* w, const vo
   const int cblk = (Cin + 255) / 256;
   const size_t esz = ufpn::dtype_size(dt);
   const size_t wt_bytes = grad_x ? static_cast<size_t>(cblk) * 256 * 256 * esz : 0;
-  const size_t zb_bytes = 1024;  // zero bias of the input-gradient launches
+  const size_t zb_bytes = static_cast<size_t>(cblk) * 256 * sizeof(float);  // zero bias of dX
   const size_t dw_bytes = grad_w ? ufpn::dw_gemm_workspace_bytes(N, H, W, Cin, 1) : 0;
   const size_t cs_bytes = grad_b ? ufpn::colsum_workspace_bytes(pixels, 256) : 0;
   StreamScratch scratch(s);
@@ -488,17 +488,14 @@ int ufpn_lateral_conv_backward(int dtype, const void* x, const void* w, const vo
     if ((e = cudaMemsetAsync(zero_bias, 0, zb_bytes, s)) != cudaSuccess) return cuda_fail(e, "memset");
     if ((e = ufpn::launch_transpose_weights(dt, w, wt, 256, Cin, cblk * 256, s)) != cudaSuccess)
       return cuda_fail(e, "transpose weights");
-    for (int cb = 0; cb < cblk; ++cb) {
-      // grad_x[:, cb*256 .. +256) = grad_out . w^T[cb*256 .. +256) : a 256-channel lateral
-      ufpn::TcPlan plan;
-      uint8_t* out = static_cast<uint8_t*>(grad_x) + static_cast<size_t>(cb) * 256 * esz;
-      const uint8_t* wslice = static_cast<const uint8_t*>(wt) + static_cast<size_t>(cb) * 256 * 256 * esz;
-      e = ufpn::plan_tc_lateral(plan, dt, grad_out, wslice, zero_bias, nullptr, out, N, 256, H, W,
-                                0, 0, ufpn::default_tiling(H, W), device_status_word(), 0);
-      if (e == cudaSuccess) e = ufpn::tc_set_output_view(plan, out, Cin - cb * 256 < 256 ? Cin - cb * 256 : 256, Cin);
-      if (e == cudaSuccess) e = ufpn::launch_tc(plan, s);
-      if (e != cudaSuccess) return cuda_fail(e, "lateral input gradient");
-    }
+    // grad_x[:, 256 cb .. +256) = grad_out . w^T[256 cb .. +256) for every slice cb: a
+    // 256-channel lateral per slice, all slices in one launch
+    ufpn::TcPlan plan;
+    e = ufpn::plan_tc_lateral(plan, dt, grad_out, wt, zero_bias, nullptr, grad_x, N, 256, H, W,
+                              0, 0, ufpn::default_tiling(H, W), device_status_word(), 0);
+    if (e == cudaSuccess) e = ufpn::tc_set_channel_slices(plan, wt, 256, cblk, grad_x, Cin);
+    if (e == cudaSuccess) e = ufpn::launch_tc(plan, s);
+    if (e != cudaSuccess) return cuda_fail(e, "lateral input gradient");
   }
   if (grad_w) {
     float* ws = reinterpret_cast<float*>(base + wt_bytes + zb_bytes);

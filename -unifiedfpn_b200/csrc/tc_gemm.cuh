@@ -158,6 +158,11 @@ struct TcGemmArgs {
   // 16-bit output: store only columns [0, out_cols) (0 = all 256), for an output view whose
   // channel slice is narrower than a tile (no TMA store then starts beyond the tensor)
   int out_cols;
+  // 16-bit lateral without a top-down add: output channel slices of 256 in one launch (0 or
+  // 1 = one).  Slice s uses weight rows [256 s, 256 s + 256), bias[256 s ..] and writes
+  // channels [256 s, 256 s + 256) of the output (columns below out_cols); the tile index runs
+  // over slices x images x tile rows x tile columns.
+  int slices;
 };
 
 template <typename T>
@@ -219,13 +224,23 @@ __device__ __forceinline__ float e4m3_scale_of(unsigned amax_bits) {
 }
 
 __device__ __forceinline__ void tc_tile_origin(const TcGemmArgs& a, int tile, int& n, int& x0,
-                                               int& y0) {
+                                               int& y0, int& slice) {
   const int tx = tile % a.tiles_x;
   const int t2 = tile / a.tiles_x;
   const int ty = t2 % a.tiles_y;
   n = t2 / a.tiles_y;
+  slice = 0;
+  if (a.slices > 1) {
+    slice = n / a.N_img;
+    n -= slice * a.N_img;
+  }
   x0 = tx * a.tile_w;
   y0 = ty * a.tile_h;
+}
+__device__ __forceinline__ void tc_tile_origin(const TcGemmArgs& a, int tile, int& n, int& x0,
+                                               int& y0) {
+  int slice;
+  tc_tile_origin(a, tile, n, x0, y0, slice);
 }
 
 // Bilinear source index along one axis (half-pixel, clamped).  Every step is an
@@ -401,8 +416,9 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
     if (!__all_sync(0xffffffffu, ok)) break;
     tc_fence_after();
 
-    int n, x0, y0;
-    tc_tile_origin(args, tile, n, x0, y0);
+    int n, x0, y0, slice;
+    tc_tile_origin(args, tile, n, x0, y0, slice);
+    const int scol = slice * kTcBlockN;  // channel offset of this tile's output slice
     const int py = y0 + row / tw;
     const int px = x0 + row % tw;
     const bool valid = real && (py < args.H) && (px < args.W);
@@ -478,7 +494,7 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
           }
         }
         float v[32];
-        const float4* b4 = reinterpret_cast<const float4*>(args.bias + c0);
+        const float4* b4 = reinterpret_cast<const float4*>(args.bias + scol + c0);
         if constexpr (kFp8) {
           const float4* s4 = reinterpret_cast<const float4*>(args.wscale + c0);
 #pragma unroll
@@ -564,9 +580,9 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
         if (lane == 0) {
           // e4m3: the warp's 128 channels (128 bytes per pixel) in one store.  Every buffer
           // use commits a group (empty for virtual tiles) so group counts stay in step.
-          if (real && (omode != 0 || args.out_cols == 0 || col0 < args.out_cols))
+          if (real && (omode != 0 || args.out_cols == 0 || scol + col0 < args.out_cols))
             tma_store_4d(map_out, my_stage + sbuf * kTcStagingPerWarp,
-                         omode == 0 ? col0 : chalf * 128, ox, oy, n);
+                         omode == 0 ? scol + col0 : chalf * 128, ox, oy, n);
           bulk_commit_group();
         }
         if (++sbuf == kStageBufs) sbuf = 0;
@@ -653,8 +669,8 @@ __global__ void __launch_bounds__(TcCfgT<kMode, T>::kThreads, 1)
     bool ok = true;
     const uint32_t coarse_bytes = static_cast<uint32_t>(args.cbox_w * args.cbox_h * 128 * 4);
     for (int tile = blockIdx.x; ok && tile < args.num_tiles; tile += gridDim.x) {
-      int n, x0, y0;
-      tc_tile_origin(args, tile, n, x0, y0);
+      int n, x0, y0, slice;
+      tc_tile_origin(args, tile, n, x0, y0, slice);
       const int nkb = args.num_kb + (bil_mma ? 1 : 0);
       for (int kb = 0; kb < nkb; ++kb) {
         ok = mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, args.status,
@@ -676,8 +692,8 @@ __global__ void __launch_bounds__(TcCfgT<kMode, T>::kThreads, 1)
             tma_load_4d(smem_a + stage * kTcAStage, &map_a, &full_bar[stage], cb * kKbElems<T>,
                         x0 + dx, y0 + dy, n,
                         kMode == 0 ? kPolicyEvictFirst : kPolicyEvictLast);
-            tma_load_2d(smem_b + stage * kTcBStage, &map_b, &full_bar[stage], kb * kKbElems<T>, 0,
-                        kPolicyEvictLast);
+            tma_load_2d(smem_b + stage * kTcBStage, &map_b, &full_bar[stage], kb * kKbElems<T>,
+                        slice * kTcBlockN, kPolicyEvictLast);
           }
         } else {
           // Bilinear k-block: Wb into the A stage (a bulk copy of the tile's precomputed

@@ -82,9 +82,9 @@ cudaError_t encode_nhwc(CUtensorMap* map, DType dt, const void* base, int N, int
 // Weights [256][K] K-major, (one 128-byte row of K, box_rows) box (256 rows, or 128 for
 // the half k-blocks of a CTA pair).
 cudaError_t encode_weights(CUtensorMap* map, DType dt, const void* base, int K,
-                           int box_rows = kTcBlockN) {
+                           int box_rows = kTcBlockN, int rows = kTcBlockN) {
   const uint64_t esz = static_cast<uint64_t>(dtype_size(dt));
-  uint64_t dims[2] = {static_cast<uint64_t>(K), kTcBlockN};
+  uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(rows)};
   uint64_t strides[1] = {static_cast<uint64_t>(K) * esz};
   uint32_t box[2] = {static_cast<uint32_t>(128 / esz), static_cast<uint32_t>(box_rows)};
   return encode(map, dt, 2, base, dims, strides, box);
@@ -457,6 +457,37 @@ cudaError_t tc_set_output_view(TcPlan& plan, void* out, int C, int pix_stride) {
   if (e != cudaSuccess) return e;
   a.out_cols = C;
   std::memcpy(plan.args, &a, sizeof(a));
+  return cudaSuccess;
+}
+
+cudaError_t tc_set_channel_slices(TcPlan& plan, const void* w, int K, int slices, void* out,
+                                  int C) {
+  if (plan.mode != 0 || plan.dtype == DType::E4M3) return cudaErrorNotSupported;
+  if (!w || !out || slices < 1 || C <= 0 || C > slices * kTcBlockN ||
+      C <= (slices - 1) * kTcBlockN)
+    return cudaErrorInvalidValue;
+  if (!aligned16(out) || !aligned16(w)) return cudaErrorMisalignedAddress;
+  TcGemmArgs a;
+  std::memcpy(&a, plan.args, sizeof(a));
+  if (a.coarse != nullptr || a.out_mode != 0 || a.amax_out != nullptr || a.slices > 1)
+    return cudaErrorNotSupported;
+  const long long tiles = static_cast<long long>(a.num_tiles) * slices;
+  if (tiles >= (1LL << 31)) return cudaErrorInvalidValue;
+  const int kb_elems = 128 / dtype_size(plan.dtype);
+  if (K <= (a.cin_blocks - 1) * kb_elems || K > a.cin_blocks * kb_elems) return cudaErrorInvalidValue;
+  cudaError_t e = encode_weights(&plan.map_b, plan.dtype, w, K, kTcBlockN, slices * kTcBlockN);
+  if (e != cudaSuccess) return e;
+  const int sw = a.tile_w < 32 ? a.tile_w : 32;
+  if ((e = encode_nhwc_map(&plan.map_out, plan.dtype, out, a.N_img, a.H, a.W, C, C, sw,
+                           32 / sw)) != cudaSuccess)
+    return e;
+  a.out_cols = C;
+  a.slices = slices;
+  a.num_tiles = static_cast<int>(tiles);
+  std::memcpy(plan.args, &a, sizeof(a));
+  plan.num_tiles = a.num_tiles;
+  const int cap = sm_count();
+  plan.grid = a.num_tiles < cap ? a.num_tiles : cap;
   return cudaSuccess;
 }
 

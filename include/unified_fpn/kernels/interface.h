@@ -205,6 +205,11 @@ cudaError_t encode_nhwc_map(CUtensorMap* map, DType dt, const void* base, int N,
 // pix_stride elements apart (out = that channel slice's first element).  Used to write the
 // 256-channel slices of a wider tensor (the input gradient of a Cin > 256 lateral).
 cudaError_t tc_set_output_view(TcPlan& plan, void* out, int C, int pix_stride);
+// One launch of a 16-bit lateral plan (no top-down add, plain output) for `slices` output
+// channel slices of 256: weights w [slices * 256][K] row-major (K = the plan's input
+// channels), bias [slices * 256], output NHWC with C channels (256 (slices - 1) < C <= 256
+// slices) at the plan's geometry.  Slice s writes channels [256 s, min(C, 256 s + 256)).
+cudaError_t tc_set_channel_slices(TcPlan& plan, const void* w, int K, int slices, void* out, int C);
 // Tiling with the fewest padded pixels for an H x W map (ties: 16 wide).
 Conv3x3Tiling default_tiling(int H, int W);
 
