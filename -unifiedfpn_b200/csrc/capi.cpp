@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <chrono>
+#include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <fstream>
@@ -199,6 +200,41 @@ int ufpn_core_set_kernel_config(ufpn_core* core, int tile_size, int channels_per
   });
 }
 
+int ufpn_core_set_activation(ufpn_core* core, int activation, float alpha) {
+  if (!core) return fail(UFPN_ERR_INVALID_ARG, "NULL core");
+  if (activation < 0 || activation > 3)
+    return fail(UFPN_ERR_INVALID_ARG, "activation must be 0 (none), 1 (ReLU), 2 (LeakyReLU) or 3 (Swish)");
+  return guarded([&] {
+    FPNKernelConfig c = core->core.get_kernel_config();
+    c.activation = static_cast<FPNActivation>(activation);
+    c.activation_alpha = alpha;
+    core->core.set_kernel_config(c);
+    return UFPN_OK;
+  });
+}
+
+int ufpn_fold_batch_norm(const float* conv_w, const float* conv_b, const float* gamma,
+                         const float* beta, const float* mean, const float* var, float eps,
+                         int Cout, long long K, float* out_w, float* out_b) {
+  if (!conv_w || !mean || !var || !out_w || !out_b)
+    return fail(UFPN_ERR_INVALID_ARG, "NULL pointer");
+  if (Cout <= 0 || K <= 0 || !(eps >= 0.f)) return fail(UFPN_ERR_INVALID_ARG, "bad sizes or eps");
+  for (int o = 0; o < Cout; ++o) {
+    if (!(var[o] + static_cast<double>(eps) > 0.0))
+      return fail(UFPN_ERR_INVALID_ARG, "var + eps must be positive");
+  }
+  for (int o = 0; o < Cout; ++o) {
+    // BN(y) = (y - mean) / sqrt(var + eps) * gamma + beta, y = W x + b: scale the row of W by
+    // s = gamma / sqrt(var + eps) and set b' = (b - mean) s + beta (double, rounded once).
+    const double sc = (gamma ? gamma[o] : 1.0) / std::sqrt(static_cast<double>(var[o]) + eps);
+    const float* wr = conv_w + static_cast<size_t>(o) * K;
+    float* orow = out_w + static_cast<size_t>(o) * K;
+    for (long long k = 0; k < K; ++k) orow[k] = static_cast<float>(wr[k] * sc);
+    out_b[o] = static_cast<float>(((conv_b ? conv_b[o] : 0.0) - mean[o]) * sc + (beta ? beta[o] : 0.0));
+  }
+  return UFPN_OK;
+}
+
 int ufpn_core_trace_next_forward(ufpn_core* core) {
   if (!core) return fail(UFPN_ERR_INVALID_ARG, "NULL core");
   core->core.trace_next_forward();
@@ -358,15 +394,24 @@ int ufpn_lateral_conv_pair(int dtype, const void* x, const void* w, const float*
 
 int ufpn_conv3x3(int dtype, const void* x, const void* w, const float* bias, void* out, void* p6,
                  int N, int H, int W, int tile_w, void* stream) {
+  return ufpn_conv3x3_act(dtype, x, w, bias, out, p6, N, H, W, tile_w, 0, 0.01f, stream);
+}
+
+int ufpn_conv3x3_act(int dtype, const void* x, const void* w, const float* bias, void* out,
+                     void* p6, int N, int H, int W, int tile_w, int activation, float alpha,
+                     void* stream) {
   DType dt;
   if (!parse_dtype(dtype, &dt)) return fail(UFPN_ERR_UNSUPPORTED, "unsupported dtype");
   if (!x || !w || !bias || !out) return fail(UFPN_ERR_INVALID_ARG, "NULL tensor pointer");
   if (N <= 0 || H <= 0 || W <= 0) return fail(UFPN_ERR_INVALID_ARG, "sizes must be positive");
+  if (activation < 0 || activation > 3)
+    return fail(UFPN_ERR_INVALID_ARG, "activation must be 0 (none), 1 (ReLU), 2 (LeakyReLU) or 3 (Swish)");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dt == DType::F32) {
     cudaError_t e = ufpn::launch_fp32_conv3x3(static_cast<const float*>(x),
                                               static_cast<const float*>(w), bias,
-                                              static_cast<float*>(out), N, 256, 256, H, W, s);
+                                              static_cast<float*>(out), N, 256, 256, H, W, s,
+                                              activation, alpha);
     if (e == cudaSuccess && p6)
       e = ufpn::launch_p6(DType::F32, out, p6, N, 256, H, W, Layout::NCHW, s);
     return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "fp32 conv3x3");
@@ -389,7 +434,10 @@ int ufpn_conv3x3(int dtype, const void* x, const void* w, const float* bias, voi
   }
   int* status = device_status_word();
   ufpn::TcPlan plan;
-  cudaError_t e = ufpn::plan_tc_conv3x3(plan, dt, x, w, bias, out, p6, N, H, W, t, status, 0);
+  ufpn::TcScales sc;
+  sc.act = activation;
+  sc.act_alpha = alpha;
+  cudaError_t e = ufpn::plan_tc_conv3x3(plan, dt, x, w, bias, out, p6, N, H, W, t, status, 0, sc);
   if (e != cudaSuccess) return cuda_fail(e, "plan conv3x3");
   e = ufpn::launch_tc(plan, s);
   return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "conv3x3 launch");

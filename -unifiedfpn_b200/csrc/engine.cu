@@ -221,6 +221,13 @@ struct UnifiedFPNCore::Impl {
   }
 
   bool tensor_core_path() const { return dtype != DType::F32 && cfg.use_tensor_cores; }
+  int act() const { return static_cast<int>(cfg.activation); }
+  ufpn::TcScales act_scales() const {
+    ufpn::TcScales sc;
+    sc.act = act();
+    sc.act_alpha = cfg.activation_alpha;
+    return sc;
+  }
 
   std::string tuning_key(int l) const {
     std::ostringstream k;
@@ -306,7 +313,7 @@ struct UnifiedFPNCore::Impl {
         if (prof_events) cudaEventRecord(prof[1 + 2 * (3 - l)], main);
         ok(ufpn::launch_fp32_conv3x3(static_cast<const float*>(merged[l]), out_w32[l], out_b[l],
                                      static_cast<float*>(out[l]), batch, cout, cout, H[l], W[l],
-                                     main),
+                                     main, act(), cfg.activation_alpha),
            "fp32 conv3x3");
         if (l == 3 && p6)
           ok(ufpn::launch_p6(DType::F32, out[3], p6, batch, cout, H[3], W[3], Layout::NCHW, main),
@@ -349,6 +356,8 @@ struct UnifiedFPNCore::Impl {
         lv[l].W = W[l];
         lv[l].lat_tiling = ufpn::default_tiling(H[l], W[l]);
         lv[l].conv_tiling = tiling_for(l);
+        lv[l].act = act();
+        lv[l].act_alpha = cfg.activation_alpha;
       }
       ufpn::NeckPlan plan;
       check(ufpn::plan_neck(plan, dtype, batch, lv, o6, d_sched, d_status, 0,
@@ -402,6 +411,8 @@ struct UnifiedFPNCore::Impl {
       lv[l].W = W[l];
       lv[l].lat_tiling = ufpn::default_tiling(H[l], W[l]);
       lv[l].conv_tiling = tiling_for(l);
+      lv[l].act = act();
+      lv[l].act_alpha = cfg.activation_alpha;
     }
     auto conv_level = [&](int l) {
       const cudaStream_t st = conv_stream(l, main, one_stream);
@@ -412,7 +423,7 @@ struct UnifiedFPNCore::Impl {
       TcPlan conv;
       check(ufpn::plan_tc_conv3x3(conv, dtype, merged[l], out_wp[l], out_b[l], o[l],
                                   l == 3 ? o6 : nullptr, batch, H[l], W[l], tiling_for(l),
-                                  d_status, 0),
+                                  d_status, 0, act_scales()),
             "plan conv3x3");
       // (on the main stream the 3x3 follows a kernel: the P2 lateral, or the previous
       // level's merge / 3x3 when every kernel runs on one stream)
@@ -569,7 +580,7 @@ struct UnifiedFPNCore::Impl {
                                       qmerged[l], fp8_scale + l * batch, conv_st,
                                       opts(pdl && conv_st == main)),
            "quantise merged map");
-      ufpn::TcScales sc;
+      ufpn::TcScales sc = act_scales();
       sc.ascale = fp8_scale + l * batch;
       sc.ascale_per_image = true;
       sc.wscale = out_ws[l];
@@ -984,8 +995,8 @@ const FPNPerformanceMetrics& UnifiedFPNCore::get_performance_metrics() const {
 }
 
 void UnifiedFPNCore::set_kernel_config(const FPNKernelConfig& config) {
-  if (config.activation != FPNActivation::NONE)
-    FPN_THROW("the standard FPN neck has no activation; only FPNActivation::NONE is supported");
+  if (static_cast<int>(config.activation) < 0 || static_cast<int>(config.activation) > 3)
+    FPN_THROW("activation must be NONE, RELU, LEAKY_RELU or SWISH");
   if (config.tile_size != 0 &&
       (config.tile_size < 1 || config.tile_size > 128 || 128 % config.tile_size != 0))
     FPN_THROW("tile_size must divide 128 (8, 16, 32, 64, 128) or be 0 for automatic");

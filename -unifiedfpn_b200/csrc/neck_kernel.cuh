@@ -32,6 +32,7 @@
 // shared-memory ring guarded by mbarriers.
 #pragma once
 
+#include "activation.cuh"
 #include "tc_gemm.cuh"
 
 namespace ufpn {
@@ -63,6 +64,8 @@ struct NeckJob {
   int dep_level;           // level whose laterals must be complete (-1: none)
   int dep_count;           // number of tiles of that lateral job
   int publish;             // lateral: a later job of this launch waits on this level
+  int act;                 // conv3x3: output activation after the bias (0 = none)
+  float act_alpha;
 };
 
 struct NeckParams {
@@ -541,6 +544,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
           }
         }
+        epilogue_act(v, jb.act, jb.act_alpha);
         if (lane == 0) bulk_wait_group_read<0>();
         __syncwarp();
 #pragma unroll

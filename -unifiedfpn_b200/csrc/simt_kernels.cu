@@ -7,6 +7,7 @@
 // coordinate (o + 0.5) * in/out - 0.5 (or o * (in-1)/(out-1) with
 // align_corners), clamped to [0, in-1], y1 = min(y0+1, in-1), weights
 // (1-wy)(1-wx), (1-wy)wx, wy(1-wx), wy*wx.
+#include "activation.cuh"
 #include "kernels.h"
 #include "ptx.cuh"
 
@@ -789,7 +790,7 @@ template <bool kIm2col>
 __global__ void __launch_bounds__(256) fp32_conv_gemm_kernel(
     const float* __restrict__ x, const float* __restrict__ wt, const float* __restrict__ bias,
     const float* __restrict__ coarse, float* __restrict__ out, int Cin, int Cout, int H, int W,
-    int Hc, int Wc, float sy_scale, float sx_scale) {
+    int Hc, int Wc, float sy_scale, float sx_scale, int act, float act_alpha) {
   __shared__ float sA[kSK][kSB + 4];  // [k][o]
   __shared__ float sB[kSK][kSB + 4];  // [k][p]
   const int HW = H * W;
@@ -857,7 +858,7 @@ __global__ void __launch_bounds__(256) fp32_conv_gemm_kernel(
         r += __ldg(cp + tp.y0 * Wc + tp.x0) * tp.w00 + __ldg(cp + tp.y0 * Wc + tp.x1) * tp.w01 +
              __ldg(cp + tp.y1 * Wc + tp.x0) * tp.w10 + __ldg(cp + tp.y1 * Wc + tp.x1) * tp.w11;
       }
-      out[(static_cast<size_t>(n) * Cout + o) * HW + p] = r;
+      out[(static_cast<size_t>(n) * Cout + o) * HW + p] = epilogue_act(r, act, act_alpha);
     }
   }
 }
@@ -1199,15 +1200,17 @@ cudaError_t launch_fp32_lateral(const float* x, const float* w, const float* bia
   const float sy = coarse ? static_cast<float>(Hc) / H : 0.f;
   const float sx = coarse ? static_cast<float>(Wc) / W : 0.f;
   fp32_conv_gemm_kernel<false>
-      <<<grid, 256, 0, s>>>(x, w, bias, coarse, out, Cin, Cout, H, W, Hc, Wc, sy, sx);
+      <<<grid, 256, 0, s>>>(x, w, bias, coarse, out, Cin, Cout, H, W, Hc, Wc, sy, sx, 0, 0.f);
   return cudaGetLastError();
 }
 
 cudaError_t launch_fp32_conv3x3(const float* x, const float* w, const float* bias, float* out,
-                                int N, int Cin, int Cout, int H, int W, cudaStream_t s) {
+                                int N, int Cin, int Cout, int H, int W, cudaStream_t s, int act,
+                                float act_alpha) {
+  if (act < 0 || act > 3) return cudaErrorInvalidValue;
   dim3 grid((H * W + kSB - 1) / kSB, (Cout + kSB - 1) / kSB, N);
-  fp32_conv_gemm_kernel<true>
-      <<<grid, 256, 0, s>>>(x, w, bias, nullptr, out, Cin, Cout, H, W, 1, 1, 0.f, 0.f);
+  fp32_conv_gemm_kernel<true><<<grid, 256, 0, s>>>(x, w, bias, nullptr, out, Cin, Cout, H, W, 1,
+                                                   1, 0.f, 0.f, act, act_alpha);
   return cudaGetLastError();
 }
 

@@ -40,6 +40,7 @@
 //                 handles 128 of the 256 output channels ((w-2)/4 selects which)
 #pragma once
 
+#include "activation.cuh"
 #include "ptx.cuh"
 
 namespace ufpn {
@@ -163,6 +164,9 @@ struct TcGemmArgs {
   // channels [256 s, 256 s + 256) of the output (columns below out_cols); the tile index runs
   // over slices x images x tile rows x tile columns.
   int slices;
+  // output activation after the bias (FPNActivation numbering; 0 = none) and its alpha
+  int act;
+  float act_alpha;
 };
 
 template <typename T>
@@ -238,9 +242,13 @@ __device__ __forceinline__ void tc_tile_origin(const TcGemmArgs& a, int tile, in
   y0 = ty * a.tile_h;
 }
 __device__ __forceinline__ void tc_tile_origin(const TcGemmArgs& a, int tile, int& n, int& x0,
-                                               int& y0) {
-  int slice;
-  tc_tile_origin(a, tile, n, x0, y0, slice);
+                                               int& y0) {  // kernels without channel slices
+  const int tx = tile % a.tiles_x;
+  const int t2 = tile / a.tiles_x;
+  const int ty = t2 % a.tiles_y;
+  n = t2 / a.tiles_y;
+  x0 = tx * a.tile_w;
+  y0 = ty * a.tile_h;
 }
 
 // Bilinear source index along one axis (half-pixel, clamped).  Every step is an
@@ -416,8 +424,11 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
     if (!__all_sync(0xffffffffu, ok)) break;
     tc_fence_after();
 
-    int n, x0, y0, slice;
-    tc_tile_origin(args, tile, n, x0, y0, slice);
+    int n, x0, y0, slice = 0;
+    if constexpr (kMode == 0 && !kPair)
+      tc_tile_origin(args, tile, n, x0, y0, slice);
+    else
+      tc_tile_origin(args, tile, n, x0, y0);
     const int scol = slice * kTcBlockN;  // channel offset of this tile's output slice
     const int py = y0 + row / tw;
     const int px = x0 + row % tw;
@@ -539,6 +550,7 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
             }
           }
         }
+        if constexpr (kMode == 1) epilogue_act(v, args.act, args.act_alpha);
         __syncwarp();
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
@@ -669,8 +681,11 @@ __global__ void __launch_bounds__(TcCfgT<kMode, T>::kThreads, 1)
     bool ok = true;
     const uint32_t coarse_bytes = static_cast<uint32_t>(args.cbox_w * args.cbox_h * 128 * 4);
     for (int tile = blockIdx.x; ok && tile < args.num_tiles; tile += gridDim.x) {
-      int n, x0, y0, slice;
-      tc_tile_origin(args, tile, n, x0, y0, slice);
+      int n, x0, y0, slice = 0;
+      if constexpr (kMode == 0)
+        tc_tile_origin(args, tile, n, x0, y0, slice);
+      else
+        tc_tile_origin(args, tile, n, x0, y0);
       const int nkb = args.num_kb + (bil_mma ? 1 : 0);
       for (int kb = 0; kb < nkb; ++kb) {
         ok = mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, args.status,

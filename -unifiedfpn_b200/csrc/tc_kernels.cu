@@ -364,6 +364,9 @@ cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w
   a.wscale = sc.wscale;
   a.amax_out = sc.amax_out;
   a.in_amax = sc.in_amax;
+  if (sc.act < 0 || sc.act > 3) return cudaErrorInvalidValue;
+  a.act = sc.act;
+  a.act_alpha = sc.act_alpha;
   const bool halo = tiling.halo;
   if (halo && (tiling.tile_w != kHaloTileW || tiling.tile_h != kHaloTileH))
     return cudaErrorInvalidValue;
@@ -589,6 +592,9 @@ cudaError_t plan_neck_jobs(NeckPlan& plan, DType dt, int N, const NeckLevel* lv,
       J.cin_blocks = kTcBlockN / kTcBlockK;
       J.num_kb = 9 * J.cin_blocks;
       J.bias = L.conv_b;
+      if (L.act < 0 || L.act > 3) return cudaErrorInvalidValue;
+      J.act = L.act;
+      J.act_alpha = L.act_alpha;
       if (lat_in_launch[l]) {
         J.dep_level = l;
         J.dep_count = lat_tiles[l];

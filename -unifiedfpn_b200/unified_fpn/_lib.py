@@ -74,6 +74,13 @@ SIGNATURES = {
                 c_int, c_int, c_void_p]),
     "ufpn_conv3x3": (
         c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
+    "ufpn_conv3x3_act": (
+        c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
+                c_float, c_void_p]),
+    "ufpn_core_set_activation": (c_int, [c_void_p, c_int, c_float]),
+    "ufpn_fold_batch_norm": (
+        c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_int, c_longlong,
+                c_void_p, c_void_p]),
     "ufpn_upsample_add": (
         c_int, [c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                 c_void_p]),

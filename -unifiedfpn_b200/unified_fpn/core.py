@@ -278,11 +278,20 @@ class UnifiedFPN:
     def set_kernel_config(self, tile_size: int = 0, channels_per_thread: int = 8, use_tensor_cores: bool = True,
                           activation: str = "none", enable_graph_capture: bool = True) -> None:
         """Reference: fpn_pytorch.cpp:189-209.  tile_size is the 3x3 tile width
-        (8..128; 0 = tuned/heuristic); only activation="none" exists in this neck."""
+        (8..128; 0 = tuned/heuristic).  ``activation`` ("relu", "leaky_relu", "swish"; any other
+        string means none, as in the reference's mapping) is applied to every level's 3x3
+        output in its epilogue; LeakyReLU uses the slope set by :meth:`set_activation`
+        (0.01 by default)."""
+        check(lib.ufpn_core_set_kernel_config(self._h, tile_size, channels_per_thread, int(use_tensor_cores),
+                                              _ACT.get(activation, 0), int(enable_graph_capture)),
+              "set_kernel_config")
+
+    def set_activation(self, activation: str = "none", alpha: float = 0.01) -> None:
+        """Output activation of every level's 3x3 (and so of P6): "none", "relu",
+        "leaky_relu" (negative slope ``alpha``) or "swish" (v / (1 + exp(-v)))."""
         if activation not in _ACT:
             raise ValueError(f"unknown activation {activation!r}")
-        check(lib.ufpn_core_set_kernel_config(self._h, tile_size, channels_per_thread, int(use_tensor_cores),
-                                              _ACT[activation], int(enable_graph_capture)), "set_kernel_config")
+        check(lib.ufpn_core_set_activation(self._h, _ACT[activation], float(alpha)), "set_activation")
 
     def set_schedule(self, fused_neck_kernel: bool = False, single_stream: bool = False,
                      programmatic_launch: bool = True, chain_priority: bool = False,

@@ -106,13 +106,21 @@ def pack_conv3x3_weight(weight: torch.Tensor, dtype: torch.dtype) -> torch.Tenso
     return out
 
 
+_ACTIVATIONS = {None: 0, "none": 0, "relu": 1, "leaky_relu": 2, "swish": 3}
+
+
 def fpn_conv3x3(input: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, p6: bool = False,
-                tile_w: int = 0):
+                tile_w: int = 0, activation: str | None = None, alpha: float = 0.01):
     """3x3 pad-1 output conv (256 -> 256) + bias; with ``p6=True`` also returns
     P6 = max_pool2d(out, 1, 2).  ``weight`` is [256, 256, 3, 3] (any float dtype)
     or, for 16-bit inputs, already packed [256, 9, 256] by :func:`pack_conv3x3_weight`.
     ``tile_w``: 0 = 8x16 halo tiles, -1 = halo tiles on CTA pairs, 8..128 = plain tiles.
+    ``activation`` ("relu", "leaky_relu" with negative slope ``alpha``, "swish") is applied
+    in the epilogue after the bias (P6 comes from the activated output); reference:
+    activation_kernel (lib/kernels/compute/fpn_compute_kernels.cu:373-395).
     """
+    if activation not in _ACTIVATIONS:
+        raise ValueError(f"unknown activation {activation!r}")
     _check_cuda(input, weight, bias)
     N, C, H, W = input.shape
     if C != 256:
@@ -130,10 +138,38 @@ def fpn_conv3x3(input: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, p
     b = bias.to(device=input.device, dtype=torch.float32).contiguous()
     out = _empty_like_layout((N, 256, H, W), x, lay)
     p6t = _empty_like_layout((N, 256, (H - 1) // 2 + 1, (W - 1) // 2 + 1), x, lay) if p6 else None
-    check(lib.ufpn_conv3x3(dt, x.data_ptr(), w.data_ptr(), b.data_ptr(), out.data_ptr(),
-                           p6t.data_ptr() if p6t is not None else None, N, H, W, tile_w,
-                           _stream(x)), "ufpn_conv3x3")
+    check(lib.ufpn_conv3x3_act(dt, x.data_ptr(), w.data_ptr(), b.data_ptr(), out.data_ptr(),
+                               p6t.data_ptr() if p6t is not None else None, N, H, W, tile_w,
+                               _ACTIVATIONS[activation], float(alpha), _stream(x)), "ufpn_conv3x3")
     return (out, p6t) if p6 else out
+
+
+def fold_batch_norm(weight: torch.Tensor, bias: torch.Tensor | None, bn_weight: torch.Tensor | None,
+                    bn_bias: torch.Tensor | None, running_mean: torch.Tensor, running_var: torch.Tensor,
+                    eps: float = 1e-5) -> tuple[torch.Tensor, torch.Tensor]:
+    """Folds an inference BatchNorm that follows a conv into the conv's weight and bias:
+    ``conv(x, W', b') == batch_norm(conv(x, W, b))`` with W' = W * s, b' = (b - mean) * s + beta,
+    s = gamma / sqrt(var + eps) per output channel (fp32 results on the CPU, computed in double
+    by the library's host code).  Reference: batch_norm_kernel
+    (lib/kernels/compute/fpn_compute_kernels.cu:342-371), run with eps 1e-5 after every output
+    conv (lib/core/fpn_engine.cu:343-353)."""
+    cout = weight.shape[0]
+
+    def host(t):
+        return None if t is None else t.detach().to(device="cpu", dtype=torch.float32).contiguous()
+
+    w = host(weight)
+    vecs = [host(t) for t in (bias, bn_weight, bn_bias, running_mean, running_var)]
+    for v in vecs:
+        if v is not None and v.numel() != cout:
+            raise ValueError("bias and BatchNorm parameters need one value per output channel")
+    out_w = torch.empty_like(w)
+    out_b = torch.empty(cout, dtype=torch.float32)
+    ptr = [None if v is None else v.data_ptr() for v in vecs]
+    check(lib.ufpn_fold_batch_norm(w.data_ptr(), ptr[0], ptr[1], ptr[2], ptr[3], ptr[4], float(eps), cout,
+                                   w.numel() // cout, out_w.data_ptr(), out_b.data_ptr()),
+          "ufpn_fold_batch_norm")
+    return out_w, out_b
 
 
 def fpn_upsample_add(coarse: torch.Tensor, lateral: torch.Tensor | None = None,

@@ -134,7 +134,11 @@ struct FPNKernelConfig {
   int shared_mem_size = 0;       // accepted for API compatibility
   bool use_tensor_cores = true;  // false forces the fp32 CUDA-core path
   bool enable_async_copy = true; // TMA is always used on the tensor-core path
+  // Output activation of every level's 3x3 (and so of P6), fused into its epilogue after the
+  // bias: NONE (the standard neck), RELU, LEAKY_RELU (negative slope activation_alpha; the
+  // reference's engine passes 0.01) or SWISH (v / (1 + exp(-v))).
   FPNActivation activation = FPNActivation::NONE;
+  float activation_alpha = 0.01f;
   bool enable_graph_capture = true;  // replay the P5->P2 schedule as one CUDA graph
   // Tensor-core path: run all 4 laterals and 4 3x3 convs as ONE persistent kernel with
   // device-side level dependencies (true), or as 8 kernels on two streams (false, the

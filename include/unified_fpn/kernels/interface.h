@@ -97,7 +97,8 @@ cudaError_t launch_fp32_lateral(const float* x, const float* w, const float* bia
                                 const float* coarse, float* out, int N, int Cin, int Cout, int H,
                                 int W, int Hc, int Wc, cudaStream_t s);
 cudaError_t launch_fp32_conv3x3(const float* x, const float* w, const float* bias, float* out,
-                                int N, int Cin, int Cout, int H, int W, cudaStream_t s);
+                                int N, int Cin, int Cout, int H, int W, cudaStream_t s,
+                                int act = 0, float act_alpha = 0.01f);
 
 // ---- tensor-core kernels (tc_kernels.cu)
 // Spatial tiling of the 3x3 implicit GEMM: tile_w * tile_h = 128 output pixels.
@@ -165,6 +166,10 @@ struct TcScales {
   // (fp32 bits); the kernel quantises each halo itself (e4m3(x * 448 / amax), the same
   // codes as launch_quantize_e4m3) and scales by amax / 448 (ascale unused).
   const unsigned* in_amax = nullptr;
+  // 3x3 only: output activation after the bias, numbered as FPNActivation (0 none, 1 ReLU,
+  // 2 LeakyReLU with act_alpha, 3 Swish); P6 is taken from the activated output.
+  int act = 0;
+  float act_alpha = 0.01f;
 };
 
 // Lateral 1x1 (+ optional fused bilinear upsample-add of the coarser merged map).
@@ -224,6 +229,8 @@ struct NeckLevel {
   void* out;            // P_l, NHWC [N][H][W][256]
   int Cin, H, W;
   Conv3x3Tiling lat_tiling, conv_tiling;
+  int act = 0;  // the level's 3x3: output activation as TcScales::act, with act_alpha
+  float act_alpha = 0.01f;
 };
 struct NeckPlan {
   alignas(64) unsigned char params[6144];  // NeckParams, opaque outside tc_kernels.cu

@@ -77,6 +77,19 @@ int ufpn_core_forward(ufpn_core* core, const void* const* inputs, void* const* o
  * FPNActivation ordinal (only NONE is supported). */
 int ufpn_core_set_kernel_config(ufpn_core* core, int tile_size, int channels_per_thread,
                                 int use_tensor_cores, int activation, int enable_graph_capture);
+/* Output activation of every level's 3x3 with its LeakyReLU slope (ufpn_core_set_kernel_config
+ * sets the activation with alpha unchanged, 0.01 by default as the reference's engine passes at
+ * fpn_engine.cu:356-358); 0 none, 1 ReLU, 2 LeakyReLU, 3 Swish. */
+int ufpn_core_set_activation(ufpn_core* core, int activation, float alpha);
+/* Host-side BatchNorm folding into a conv: for each output channel o, s = gamma[o] /
+ * sqrt(var[o] + eps), out_w[o][k] = conv_w[o][k] * s, out_b[o] = (conv_b[o] - mean[o]) * s +
+ * beta[o] (conv_b, gamma, beta may be NULL: 0, 1, 0), so conv(out_w, out_b) equals
+ * batch_norm_kernel applied to conv(conv_w, conv_b) (fpn_compute_kernels.cu:342-371, called
+ * with eps 1e-5 at fpn_engine.cu:343-353).  K = weights per output channel (Cin * kh * kw);
+ * host pointers; out_w / out_b may alias conv_w / conv_b. */
+int ufpn_fold_batch_norm(const float* conv_w, const float* conv_b, const float* gamma,
+                         const float* beta, const float* mean, const float* var, float eps,
+                         int Cout, long long K, float* out_w, float* out_b);
 /* Tensor-core schedule: 1 = one persistent kernel for the whole neck, 0 = per-level kernels
  * on two streams (default), 2 = the same kernels one after the other on the caller's stream.
  * No reference counterpart (its engine launched 16 kernels on four unordered streams,
@@ -145,6 +158,13 @@ int ufpn_lateral_conv_pair(int dtype, const void* x, const void* w, const float*
  * plain tiles of that width (one box per tap). */
 int ufpn_conv3x3(int dtype, const void* x, const void* w, const float* bias, void* out,
                  void* p6, int N, int H, int W, int tile_w, void* stream);
+/* ufpn_conv3x3 with an output activation fused into its epilogue after the bias (P6, if
+ * asked for, is taken from the activated output): activation 0 none, 1 ReLU, 2 LeakyReLU
+ * (negative slope alpha), 3 Swish (v / (1 + exp(-v))).  Replaces launch_output_conv's
+ * separate activation_kernel pass (fpn_engine.cu:356-358; fpn_compute_kernels.cu:373-395). */
+int ufpn_conv3x3_act(int dtype, const void* x, const void* w, const float* bias, void* out,
+                     void* p6, int N, int H, int W, int tile_w, int activation, float alpha,
+                     void* stream);
 
 /* out = lateral + bilinear_upsample(coarse -> H x W); lateral may be NULL (pure upsample).
  * Replaces launch_upsample_and_add (fpn_engine.cu:274-313) = bilinear_upsample_kernel +

@@ -26,6 +26,12 @@ What it restates (paths relative to the sanowl/-UnifiedFPN source tree):
   per-output-channel scales = absmax / 448), quantising each merged map before its
   3x3 and storing bf16 where the CUDA schedule does; ``e4m3_round`` is the
   nearest-even e4m3fn rounding, pinned against torch's float8_e4m3fn conversion.
+* ``activation`` -- activation_kernel (lib/kernels/compute/fpn_compute_kernels.cu:373-395):
+  ReLU max(0, v), LeakyReLU v > 0 ? v : alpha v, Swish v / (1 + exp(-v)); the LeakyReLU
+  formula is the one the reference's unit test checks (tests/unit/test_fpn_kernels.cu:270-300).
+  ``fpn_neck(act=...)`` applies it to every 3x3 output (P6 taken after it).
+* ``batch_norm`` -- batch_norm_kernel (fpn_compute_kernels.cu:342-371):
+  (v - mean) / sqrt(var + eps) * gamma + beta per channel (eps 1e-5 at fpn_engine.cu:343-353).
 
 Tolerances (fp32 <= 1e-4, bf16/fp16 <= 1e-2, FP8 <= 3e-2) are relative to the
 largest magnitude of the reference output: ``rel_err(y, ref) = max|y - ref| / max|ref|``.
@@ -96,6 +102,31 @@ def p6_maxpool(p5: torch.Tensor) -> torch.Tensor:
     return F.max_pool2d(p5, kernel_size=1, stride=2)
 
 
+def activation(x: torch.Tensor, kind: str | None, alpha: float = 0.01) -> torch.Tensor:
+    """activation_kernel (fpn_compute_kernels.cu:373-395), elementwise in x's dtype."""
+    if kind in (None, "none"):
+        return x
+    if kind == "relu":
+        return torch.clamp_min(x, 0.0)
+    if kind == "leaky_relu":
+        return torch.where(x > 0, x, alpha * x)
+    if kind == "swish":
+        return x / (1.0 + torch.exp(-x))
+    raise ValueError(kind)
+
+
+def batch_norm(x: torch.Tensor, gamma, beta, mean, var, eps: float = 1e-5) -> torch.Tensor:
+    """batch_norm_kernel (fpn_compute_kernels.cu:342-371) on NCHW: per channel c,
+    (x - mean[c]) / sqrt(var[c] + eps) * gamma[c] + beta[c] (gamma / beta None: 1 / 0)."""
+    sh = (1, -1, 1, 1)
+    y = (x - mean.reshape(sh)) / torch.sqrt(var.reshape(sh) + eps)
+    if gamma is not None:
+        y = y * gamma.reshape(sh)
+    if beta is not None:
+        y = y + beta.reshape(sh)
+    return y
+
+
 @dataclass
 class NeckWeights:
     lat_w: list  # [256, Cin] fp32
@@ -104,8 +135,10 @@ class NeckWeights:
     out_b: list  # [256]
 
 
-def fpn_neck(feats, wts: NeckWeights, return_merged: bool = False):
-    """fp32 CPU neck.  feats: C2..C5 (NCHW float tensors).  Returns [P2, P3, P4, P5, P6]."""
+def fpn_neck(feats, wts: NeckWeights, return_merged: bool = False, act: str | None = None,
+             alpha: float = 0.01):
+    """fp32 CPU neck.  feats: C2..C5 (NCHW float tensors).  Returns [P2, P3, P4, P5, P6];
+    ``act`` is applied to each 3x3 output before P6 is taken."""
     feats = [f.float() for f in feats]
     merged = [None] * 4
     for l in (3, 2, 1, 0):
@@ -113,7 +146,8 @@ def fpn_neck(feats, wts: NeckWeights, return_merged: bool = False):
         if l < 3:
             m = m + bilinear_upsample_t(merged[l + 1], m.shape[-2:])
         merged[l] = m
-    outs = [conv3x3(merged[l], wts.out_w[l].float(), wts.out_b[l].float()) for l in range(4)]
+    outs = [activation(conv3x3(merged[l], wts.out_w[l].float(), wts.out_b[l].float()), act, alpha)
+            for l in range(4)]
     outs.append(p6_maxpool(outs[3]))
     return (outs, merged) if return_merged else outs
 
@@ -264,7 +298,8 @@ def _bf16(x: torch.Tensor) -> torch.Tensor:
     return x.to(torch.bfloat16).float()
 
 
-def fpn_neck_e4m3(q_feats, in_scales, qw: NeckWeightsE4M3, return_merged: bool = False):
+def fpn_neck_e4m3(q_feats, in_scales, qw: NeckWeightsE4M3, return_merged: bool = False,
+                  act: str | None = None, alpha: float = 0.01):
     """FP8 neck with the storage points of the CUDA schedule: e4m3 inputs C_l = q_l * s_l;
     laterals in fp64 from the codes, scaled by s_l * w_scale[o] (+ bias) and stored bf16;
     M_l = bf16(L_l + up(M_{l+1})) (P2: one rounding of L_2 + up(M_3)); each M_l quantised
@@ -295,8 +330,8 @@ def fpn_neck_e4m3(q_feats, in_scales, qw: NeckWeightsE4M3, return_merged: bool =
         q, s = quantize_e4m3_images(merged[l])
         acc = F.conv2d(torch.from_numpy(q).double(), qw.out_q[l].double(), padding=1)
         cs = (torch.from_numpy(s).reshape(-1, 1) * qw.out_s[l].reshape(1, -1)).double()  # fp32
-        outs.append(_bf16((acc * cs.reshape(cs.shape[0], -1, 1, 1)
-                           + qw.out_b[l].double().reshape(1, -1, 1, 1)).float()))
+        outs.append(_bf16(activation((acc * cs.reshape(cs.shape[0], -1, 1, 1)
+                                      + qw.out_b[l].double().reshape(1, -1, 1, 1)).float(), act, alpha)))
     outs.append(p6_maxpool(outs[3]))
     return (outs, merged) if return_merged else outs
 

@@ -65,6 +65,9 @@ def test_host_side_argument_validation():
     assert lib.ufpn_upsample_add(2, 1, 16, None, 16, 1, 256, -1, 2, 4, 4, 0, None) == _lib.ERR_INVALID_ARG
     # conv3x3 tile width must divide 128
     assert lib.ufpn_conv3x3(2, 16, 16, 16, 16, None, 1, 8, 8, 24, None) == _lib.ERR_INVALID_ARG
+    # activation codes are 0..3
+    assert lib.ufpn_conv3x3_act(2, 16, 16, 16, 16, None, 1, 8, 8, 0, 7, 0.01, None) == _lib.ERR_INVALID_ARG
+    assert lib.ufpn_core_set_activation(None, 1, 0.01) == _lib.ERR_INVALID_ARG
     # engine calls on a NULL handle
     assert lib.ufpn_core_forward(None, None, None, None, None) == _lib.ERR_INVALID_ARG
     assert lib.ufpn_core_get_memory_usage(None) == 0

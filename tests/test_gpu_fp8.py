@@ -250,3 +250,16 @@ def test_fp8_errors(cuda_device):
     with pytest.raises(ValueError):
         fpn([torch.zeros(1, c, 8, 8, device="cuda", dtype=torch.bfloat16) for c in O.R50_CHANNELS],
             input_scales=[1.0] * 4)             # scales for a 16-bit neck
+
+
+def test_fp8_neck_activation(cuda_device):
+    """LeakyReLU on the e4m3 neck's 3x3 outputs (applied to the scaled fp32 value before the
+    bf16 store) against the e4m3 oracle with the same activation."""
+    import unified_fpn as U
+    feats, wts, qf, sc = _fp8_case(2, O.R50_CHANNELS, O.level_sizes(128, 192), seed=31)
+    fpn = U.UnifiedFPN()
+    fpn.set_activation("leaky_relu", 0.1)
+    _, _, outs = _run_fp8_neck(O.R50_CHANNELS, wts, qf, sc, fpn=fpn)
+    ref = O.fpn_neck_e4m3(qf, sc, O.quantize_neck_weights(wts), act="leaky_relu", alpha=0.1)
+    for o, r in zip(outs, ref):
+        assert O.rel_err(o.float().cpu(), r) < TOL8

@@ -307,3 +307,30 @@ def test_layout_convert_roundtrip(cuda_device):
     assert _lib.lib.ufpn_layout_convert(2, y.data_ptr(), z.data_ptr(), 2, 40, 7, 9, 0, s) == 0
     assert torch.equal(y, x.permute(0, 2, 3, 1))
     assert torch.equal(z, x)
+
+
+@pytest.mark.parametrize("dtype,tile_w", [(torch.bfloat16, 0), (torch.bfloat16, -1), (torch.float16, 16),
+                                          (torch.float32, 0)])
+@pytest.mark.parametrize("act,alpha", [("relu", 0.01), ("leaky_relu", 0.2), ("swish", 0.01)])
+def test_conv3x3_activation_epilogue(cuda_device, dtype, tile_w, act, alpha):
+    """The activation fused into the 3x3 epilogue after the bias (P6 taken from the activated
+    output) against the oracle's conv3x3 followed by the reference's activation formula."""
+    import unified_fpn as U
+    g = torch.Generator().manual_seed(len(act) * 7 + tile_w)
+    x = torch.randn(2, 256, 13, 21, generator=g).to(dtype)
+    w = torch.randn(256, 256, 3, 3, generator=g) * (2.0 / 2304) ** 0.5
+    b = torch.rand(256, generator=g) * 0.2 - 0.1
+    xd = x.to(cuda_device)
+    if dtype != torch.float32:
+        xd = _cl(xd)
+    y, p6 = U.fpn_conv3x3(xd, w.to(cuda_device), b.to(cuda_device), p6=True, tile_w=tile_w,
+                          activation=act, alpha=alpha)
+    torch.cuda.synchronize()
+    assert U.device_status() == 0
+    ref = O.activation(O.conv3x3(x.float(), w.to(dtype).float(), b), act, alpha)
+    assert O.rel_err(y.float().cpu(), ref) < (F32_TOL if dtype == torch.float32 else BF16_TOL)
+    assert torch.equal(p6.cpu(), y.cpu()[:, :, ::2, ::2])
+    if act == "relu":
+        assert y.min().item() >= 0
+    with pytest.raises(ValueError):
+        U.fpn_conv3x3(xd, w.to(cuda_device), b.to(cuda_device), activation="gelu")

@@ -256,3 +256,37 @@ def test_schedule_options_are_bitwise_equal(cuda_device, fp8):
             assert torch.equal(a, b), (pl, pr, m2)
         if m2 and not fp8:
             assert int(fpn.get_performance_breakdown(feats, input_scales=sc)[1][4].item()) == 7
+
+
+@pytest.mark.parametrize("act,alpha", [("relu", 0.01), ("leaky_relu", 0.1), ("swish", 0.01)])
+@pytest.mark.parametrize("mode", ["split", "fused", "fp32"])
+def test_neck_activation(cuda_device, act, alpha, mode):
+    """set_activation: every level's 3x3 output (and P6) activated in the epilogue, on the
+    split and fused tensor-core schedules and the fp32 path, against the oracle neck."""
+    import unified_fpn as U
+    dtype = torch.float32 if mode == "fp32" else torch.bfloat16
+    chans = (64, 128, 256, 256) if mode == "fp32" else O.R50_CHANNELS
+    feats = O.make_features(2, chans, O.level_sizes(96, 160), seed=4, dist="normal")
+    wts = O.make_weights(chans, seed=5, bias_scale=0.1)
+    fpn = U.UnifiedFPN()
+    fpn.set_schedule(fused_neck_kernel=mode == "fused")
+    fpn.set_activation(act, alpha)
+    fpn.initialize_weights(wts.lat_w, wts.lat_b, wts.out_w, wts.out_b)
+    xin = [f.to(dtype).to(cuda_device) for f in feats]
+    if dtype != torch.float32:
+        xin = [_cl(x) for x in xin]
+    outs = _run(fpn, xin)
+    assert fpn.device_status() == 0
+    if dtype == torch.float32:
+        ref = O.fpn_neck(feats, wts, act=act, alpha=alpha)
+    else:
+        rw = O.NeckWeights([O.round_to(w, dtype) for w in wts.lat_w], wts.lat_b,
+                           [O.round_to(w, dtype) for w in wts.out_w], wts.out_b)
+        ref = O.fpn_neck([O.round_to(f, dtype) for f in feats], rw, act=act, alpha=alpha)
+    _check(outs, ref, TOL32 if dtype == torch.float32 else TOL16)
+    # back to the standard neck through the reference's string mapping (unknown -> none)
+    fpn.set_kernel_config(activation="not-an-activation")
+    plain = _run(fpn, xin)
+    ref0 = O.fpn_neck(feats, wts) if dtype == torch.float32 else O.fpn_neck(
+        [O.round_to(f, dtype) for f in feats], rw)
+    _check(plain, ref0, TOL32 if dtype == torch.float32 else TOL16)
