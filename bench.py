@@ -1,6 +1,7 @@
 """Benchmark: FPN-neck images/s on B200 (R50 800x1216, bf16, batch 2 per GPU).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  python bench.py --train [--dtype bf16|fp16] ...   (training step: forward + backward)
 
 One step = one forward of the whole neck (4 fused laterals + 4 implicit-GEMM 3x3
 convs + P6) over one batch.  Multi-GPU (torchrun, one process per GPU): every
@@ -13,6 +14,11 @@ Prints ONE JSON line (rank 0).  Keys beyond the base contract:
   roofline    the dominant kernel (P2 3x3 implicit GEMM) timed live with CUDA events
   cpu_baseline  the CPU oracle neck (fp32 torch CPU, all host threads) on a bounded sample
   clocks      nvidia-smi samples taken during the timed window
+
+--train times the neck's training step instead (its own JSON line, metric METRIC_TRAIN): the
+forward of unified_fpn.FPNNeck (fp32 master weights, 16-bit kernels) and the backward to every
+input, weight and bias gradient, for seeded gradients of P2..P6; gradients are reset to None
+between steps (no accumulation adds).  Not the headline metric.
 """
 from __future__ import annotations
 
@@ -33,7 +39,15 @@ import torch  # noqa: E402
 
 METRIC = "FPN-neck images/sec, R50 800×1216 bf16 @1/2/4/8 B200; % of roofline"
 METRIC_FP8 = "FPN-neck images/sec, FP8 (e4m3) R50 640×640, 16 images/GPU @1/2/4/8 B200; % of roofline"
+METRIC_TRAIN = "FPN-neck training steps (forward + backward, all gradients) images/sec, R50 800×1216"
 R50_CHANNELS = (256, 512, 1024, 2048)
+# Library kernels per training step (FPNNeck forward + backward with gradients for P2..P6):
+# forward per level: 3x3 weight packing, lateral (with the fused top-down add), 3x3 (+P6);
+# backward per level: 3x3 weight flip, input gradient, weight-gradient GEMM + its reduction,
+# bias column sums + their row reduction; lateral: weight transpose, input gradient (one launch
+# for all channel slices), weight-gradient GEMM + reduction, bias sums + reduction; the P6
+# adjoint once and the top-down adjoint for P3, P4, P5.
+TRAIN_LAUNCHES = 4 * 3 + 4 * 6 + 4 * 6 + 1 + 3
 
 
 def level_sizes(h, w):
@@ -204,6 +218,92 @@ def run_reference(args, rank, world):
     return 0
 
 
+def run_train(args, rank, world, local, dev):
+    """Training-step throughput: FPNNeck forward + backward over 3 rotating input sets."""
+    import torch.distributed as dist
+    import unified_fpn as U
+
+    dtype = {"bf16": torch.bfloat16, "fp16": torch.float16}[args.dtype]
+    sizes = level_sizes(args.height, args.width)
+    B = args.batch
+    n_sets = 3
+    gen = torch.Generator(device=dev)
+    feats, grads = [], []
+    for s in range(n_sets):
+        gen.manual_seed(1000 * rank + s)
+        feats.append([torch.randn(B, c, h, w, device=dev, generator=gen).clamp_min_(0).to(dtype)
+                      .contiguous(memory_format=torch.channels_last).requires_grad_()
+                      for c, (h, w) in zip(R50_CHANNELS, sizes)])
+        out_sizes = list(sizes) + [((sizes[3][0] - 1) // 2 + 1, (sizes[3][1] - 1) // 2 + 1)]
+        grads.append([torch.randn(B, 256, h, w, device=dev, generator=gen).to(dtype)
+                      .contiguous(memory_format=torch.channels_last) for h, w in out_sizes])
+    in_mb = sum(B * c * h * w * 2 for c, (h, w) in zip(R50_CHANNELS, sizes)) / 1e6
+    neck = U.FPNNeck(R50_CHANNELS).to(dev)
+
+    def step(i):
+        k = i % n_sets
+        for p in neck.parameters():
+            p.grad = None
+        for f in feats[k]:
+            f.grad = None
+        outs = neck(feats[k])
+        torch.autograd.backward(outs, grads[k])
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize(dev)
+    if U.device_status() != 0:
+        raise RuntimeError("device pipeline timeout during warm-up")
+    stream = torch.cuda.current_stream(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    clocks.start()
+    time.sleep(0.3)
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    ms, images = job_throughput(e0.elapsed_time(e1), B * args.steps, world, dev)
+    ms_per_step = ms / args.steps
+    peaks = measured_peaks()
+    flops = 3.0 * neck_flops(B, R50_CHANNELS, sizes)  # forward + input and weight gradients
+    achieved = flops / (ms_per_step * 1e-3) / 1e12
+    if rank == 0:
+        line = {
+            "metric": METRIC_TRAIN, "value": round(images / (ms / 1e3), 2), "unit": "images/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_per_step, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": args.dtype,
+            "data": "synthetic (seeded N(0,1) after ReLU clamp; seeded N(0,1) output gradients; "
+                    "random Kaiming-normal fp32 master weights)",
+            "config": {"workload": f"R50 FPN neck training step {args.height}x{args.width}, {B} images/GPU, "
+                                   f"{args.dtype} NHWC, gradients of every input, weight and bias",
+                       "global_batch": B * world, "per_gpu_batch": B,
+                       "l2": f"inputs rotate over {n_sets} sets ({n_sets} x {in_mb:.0f} MB) > 126 MB L2",
+                       "parallelism": f"dp{world} batch shards (gradients not reduced)"},
+            "clocks": clk, "gpu_launches": TRAIN_LAUNCHES * args.steps,
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 1),
+                         "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                         "frac": round(achieved / peaks["bf16_tflops_sustained"], 4),
+                         "flops_per_step": flops, "peak_source": peaks["src"] + " (sustained)",
+                         "traffic": None},
+            "device_status": U.device_status(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -223,7 +323,11 @@ def main():
     ap.add_argument("--schedule", choices=["fused", "split", "serial"], default="split",
                     help="one persistent neck kernel, per-level kernels on two streams, or the "
                          "per-level kernels one after the other on one stream")
+    ap.add_argument("--train", action="store_true",
+                    help="time the training step (FPNNeck forward + backward) instead")
     args = ap.parse_args()
+    if args.train and args.dtype == "e4m3":
+        ap.error("--train runs on bf16 or fp16")
     fp8 = args.dtype == "e4m3"
     if args.batch is None:
         args.batch = 16 if fp8 else 2
@@ -249,6 +353,8 @@ def main():
 
     import unified_fpn as U
 
+    if args.train:
+        return run_train(args, rank, world, local, dev)
     fp8 = args.dtype == "e4m3"
     dtype = {"bf16": torch.bfloat16, "fp16": torch.float16, "e4m3": torch.float8_e4m3fn}[args.dtype]
     esz = 1 if fp8 else 2
