@@ -65,6 +65,16 @@ def test_host_side_argument_validation():
     assert lib.ufpn_upsample_add(2, 1, 16, None, 16, 1, 256, -1, 2, 4, 4, 0, None) == _lib.ERR_INVALID_ARG
     # conv3x3 tile width must divide 128
     assert lib.ufpn_conv3x3(2, 16, 16, 16, 16, None, 1, 8, 8, 24, None) == _lib.ERR_INVALID_ARG
+    # backward: 16-bit only, NULL gradients, Cin a multiple of 8, alignment, shapes (all checked
+    # on the host before any launch)
+    assert lib.ufpn_lateral_conv_backward(0, 16, 16, 16, 16, None, None, 1, 64, 2, 2, None) == _lib.ERR_UNSUPPORTED
+    assert lib.ufpn_lateral_conv_backward(2, None, None, None, None, None, None, 1, 64, 2, 2, None) == \
+        _lib.ERR_INVALID_ARG
+    assert lib.ufpn_lateral_conv_backward(2, None, None, 16, None, None, None, 1, 12, 2, 2, None) == \
+        _lib.ERR_UNSUPPORTED
+    assert lib.ufpn_conv3x3_backward(2, 16, 16, 18, 16, None, None, 1, 4, 4, None) == _lib.ERR_ALIGNMENT
+    assert lib.ufpn_upsample_add_backward(2, 16, None, 16, 1, 256, 8, 8, 4, 4, None) == _lib.ERR_UNSUPPORTED
+    assert lib.ufpn_p6_backward(2, 16, 16, 1, 256, -3, 4, None) == _lib.ERR_INVALID_ARG
     # activation codes are 0..3
     assert lib.ufpn_conv3x3_act(2, 16, 16, 16, 16, None, 1, 8, 8, 0, 7, 0.01, None) == _lib.ERR_INVALID_ARG
     assert lib.ufpn_core_set_activation(None, 1, 0.01) == _lib.ERR_INVALID_ARG
