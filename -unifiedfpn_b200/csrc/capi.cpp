@@ -200,6 +200,16 @@ int ufpn_core_set_kernel_config(ufpn_core* core, int tile_size, int channels_per
   });
 }
 
+int ufpn_core_set_fp8_options(ufpn_core* core, int two_pass_p2) {
+  if (!core) return fail(UFPN_ERR_INVALID_ARG, "NULL core");
+  return guarded([&] {
+    FPNKernelConfig c = core->core.get_kernel_config();
+    c.fp8_two_pass_p2 = two_pass_p2 != 0;
+    core->core.set_kernel_config(c);
+    return UFPN_OK;
+  });
+}
+
 int ufpn_core_set_activation(ufpn_core* core, int activation, float alpha) {
   if (!core) return fail(UFPN_ERR_INVALID_ARG, "NULL core");
   if (activation < 0 || activation > 3)

@@ -539,16 +539,23 @@ struct UnifiedFPNCore::Impl {
       check(cudaEventRecord(ev_fork, main), "event");
       for (int i = 0; i < 2; ++i) check(cudaStreamWaitEvent(lat_side[i], ev_fork, 0), "event");
     }
+    // out_mode: 0 store bf16 M_l (and its absmax into amax_out, if given), 1 publish only the
+    // absmax, 2 store M_l quantised to e4m3 (qmerged[l]) with the absmax of pass 1.
     auto lateral = [&](int l, const void* coarse, unsigned* amax_out, cudaStream_t st,
-                       bool after_kernel) {
+                       bool after_kernel, int out_mode = 0) {
       ufpn::TcScales sc;
       sc.ascale = in_scale[l];
       sc.wscale = lat_ws[l];
-      sc.amax_out = amax_out;
+      sc.amax_out = out_mode == 2 ? nullptr : amax_out;
       sc.coarse_prescaled = coarse != nullptr;  // coarse = m3_scaled
+      sc.out_mode = out_mode;
+      if (out_mode == 2) {
+        sc.qamax = fp8_amax + l * batch;
+        sc.qscale_out = fp8_scale + l * batch;
+      }
       TcPlan p;
       // (with lat4_raw, L4 goes there: the two-level merge writes M4)
-      void* lout = (l == 2 && two_level) ? lat4_raw : merged[l];
+      void* lout = out_mode == 2 ? qmerged[l] : (l == 2 && two_level) ? lat4_raw : merged[l];
       check(ufpn::plan_tc_lateral(p, DType::E4M3, in[l], lat_wp[l], lat_b[l], coarse, lout,
                                   batch, cin[l], H[l], W[l], coarse ? H[l + 1] : 0,
                                   coarse ? W[l + 1] : 0, ufpn::default_tiling(H[l], W[l]),
@@ -639,9 +646,15 @@ struct UnifiedFPNCore::Impl {
         if (prof_events) cudaEventRecord(prof[4 + 2 * (2 - l)], main);
       }
     }
-    lateral(0, m3_scaled, fp8_amax, main, true);
+    if (cfg.fp8_two_pass_p2) {
+      // P2: absmax pass, then the quantised store -- M2 never exists in bf16 in HBM
+      lateral(0, m3_scaled, fp8_amax, main, true, 1);
+      lateral(0, m3_scaled, nullptr, main, true, 2);
+    } else {
+      lateral(0, m3_scaled, fp8_amax, main, true);
+    }
     if (prof_events) cudaEventRecord(prof[7], main);
-    conv_level(0);
+    conv_level(0, !cfg.fp8_two_pass_p2);
     if (prof_events) cudaEventRecord(prof[8], main);
     if (!one_stream) join_conv_streams(main);
     return launches;

@@ -574,6 +574,15 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
             st_shared_v4(stage_addr + lane * 128 + ((j ^ (lane & 7)) << 4), o);
             if (emit_p6)
               reinterpret_cast<uint4*>(p6_row + static_cast<size_t>(col0) * sizeof(O))[j] = o;
+          } else if (kSteps == 1 && omode == 2) {
+            // 8 channels -> 8 e4m3 bytes, half of 16-byte chunk j / 2 of the warp's 64-byte
+            // row; the 64-byte swizzle puts chunk c of row r at c ^ ((r >> 1) & 3)
+            const float2 f0 = Pack<O>::unpack(o.x), f1 = Pack<O>::unpack(o.y);
+            const float2 f2 = Pack<O>::unpack(o.z), f3 = Pack<O>::unpack(o.w);
+            const uint32_t q0 = tc_e4m3x4(f0.x, f0.y, f1.x, f1.y, qinv);
+            const uint32_t q1 = tc_e4m3x4(f2.x, f2.y, f3.x, f3.y, qinv);
+            const int chunk = (j >> 1) ^ ((lane >> 1) & 3);
+            st_shared_v2(stage_addr + lane * 64 + (chunk << 4) + (j & 1) * 8, q0, q1);
           } else if (kSteps == 2 && omode == 2) {
             // 8 channels -> 8 e4m3 bytes, half of 16-byte chunk (step * 4 + j / 2) of the row
             const float2 f0 = Pack<O>::unpack(o.x), f1 = Pack<O>::unpack(o.y);
@@ -594,7 +603,7 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
           // use commits a group (empty for virtual tiles) so group counts stay in step.
           if (real && (omode != 0 || args.out_cols == 0 || scol + col0 < args.out_cols))
             tma_store_4d(map_out, my_stage + sbuf * kTcStagingPerWarp,
-                         omode == 0 ? scol + col0 : chalf * 128, ox, oy, n);
+                         omode == 0 ? scol + col0 : chalf * kChans, ox, oy, n);
           bulk_commit_group();
         }
         if (++sbuf == kStageBufs) sbuf = 0;

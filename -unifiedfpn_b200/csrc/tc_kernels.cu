@@ -43,9 +43,11 @@ CUtensorMapDataType tmap_dtype(DType dt) {
   }
 }
 
-// rank-d tiled map with 128-byte swizzle; dims/strides innermost first, strides in bytes.
+// rank-d tiled map with 128-byte swizzle (64-byte for a 64-byte inner box); dims/strides
+// innermost first, strides in bytes.
 cudaError_t encode(CUtensorMap* map, DType dt, int rank, const void* base, const uint64_t* dims,
-                   const uint64_t* strides, const uint32_t* box) {
+                   const uint64_t* strides, const uint32_t* box,
+                   CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   auto fn = encode_fn();
   if (!fn) return cudaErrorNotSupported;
   if (!aligned16(base)) return cudaErrorMisalignedAddress;
@@ -61,22 +63,25 @@ cudaError_t encode(CUtensorMap* map, DType dt, int rank, const void* base, const
   }
   for (int i = 0; i + 1 < rank; ++i) st[i] = strides[i];
   CUresult r = fn(map, tmap_dtype(dt), rank, const_cast<void*>(base), d, st, b, es,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-// NHWC activation map [N][H][W][C] with a (one 128-byte row of channels, bw, bh, 1) box.
+// NHWC activation map [N][H][W][C] with a (one 128-byte row of channels, bw, bh, 1) box, or
+// with inner_bytes = 64 a 64-byte row of channels under the 64-byte swizzle (16-byte chunk c
+// of box row r at chunk c ^ ((r >> 1) & 3)).
 cudaError_t encode_nhwc(CUtensorMap* map, DType dt, const void* base, int N, int H, int W, int C,
-                        int bw, int bh) {
+                        int bw, int bh, int inner_bytes = 128) {
   const uint64_t esz = static_cast<uint64_t>(dtype_size(dt));
   uint64_t dims[4] = {static_cast<uint64_t>(C), static_cast<uint64_t>(W),
                       static_cast<uint64_t>(H), static_cast<uint64_t>(N)};
   uint64_t strides[3] = {static_cast<uint64_t>(C) * esz, static_cast<uint64_t>(W) * C * esz,
                          static_cast<uint64_t>(H) * W * C * esz};
-  uint32_t box[4] = {static_cast<uint32_t>(128 / esz), static_cast<uint32_t>(bw),
+  uint32_t box[4] = {static_cast<uint32_t>(inner_bytes / esz), static_cast<uint32_t>(bw),
                      static_cast<uint32_t>(bh), 1};
-  return encode(map, dt, 4, base, dims, strides, box);
+  return encode(map, dt, 4, base, dims, strides, box,
+                inner_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 // Weights [256][K] K-major, (one 128-byte row of K, box_rows) box (256 rows, or 128 for
@@ -248,9 +253,10 @@ cudaError_t plan_tc_lateral(TcPlan& plan, DType dt, const void* x, const void* w
   if (!valid_tiling(tiling)) return cudaErrorInvalidValue;
   if (coarse && (Hc <= 0 || Wc <= 0)) return cudaErrorInvalidValue;
   if (fp8 && (!sc.ascale || !sc.wscale)) return cudaErrorInvalidValue;
-  // (out_mode 2 assembles 128-byte e4m3 rows from two 64-channel steps per warp; the
-  // lateral's 16 epilogue warps own 64 channels each, so it is not available here.)
-  if (sc.out_mode < 0 || sc.out_mode > 1 || (sc.out_mode == 1 && !sc.amax_out))
+  // (out_mode 2: each of the lateral's 16 epilogue warps stores its 64 channels as 64-byte
+  // e4m3 rows through a map with a 64-byte box and the 64-byte swizzle.)
+  if (sc.out_mode < 0 || sc.out_mode > 2 || (sc.out_mode == 1 && !sc.amax_out) ||
+      (sc.out_mode == 2 && (!sc.qamax || !sc.qscale_out)))
     return cudaErrorInvalidValue;
   if (!aligned16(out) || (coarse && !aligned16(coarse)) || !aligned16(bias) ||
       (fp8 && !aligned16(sc.wscale)))
@@ -277,7 +283,7 @@ cudaError_t plan_tc_lateral(TcPlan& plan, DType dt, const void* x, const void* w
   if ((e = encode_weights(&plan.map_b, dt, w, Cin)) != cudaSuccess) return e;
   const int sw = tiling.tile_w < 32 ? tiling.tile_w : 32;
   if ((e = encode_nhwc(&plan.map_out, sc.out_mode == 2 ? DType::E4M3 : odt, out, N, H, W,
-                       kTcBlockN, sw, 32 / sw)) != cudaSuccess)
+                       kTcBlockN, sw, 32 / sw, sc.out_mode == 2 ? 64 : 128)) != cudaSuccess)
     return e;
   plan.map_coarse = plan.map_out;  // unused unless a coarse map is staged
   if (coarse) {

@@ -78,6 +78,7 @@ SIGNATURES = {
         c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
                 c_float, c_void_p]),
     "ufpn_core_set_activation": (c_int, [c_void_p, c_int, c_float]),
+    "ufpn_core_set_fp8_options": (c_int, [c_void_p, c_int]),
     "ufpn_fold_batch_norm": (
         c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_int, c_longlong,
                 c_void_p, c_void_p]),

@@ -295,7 +295,7 @@ class UnifiedFPN:
 
     def set_schedule(self, fused_neck_kernel: bool = False, single_stream: bool = False,
                      programmatic_launch: bool = True, chain_priority: bool = False,
-                     merge_two_levels: bool = False) -> None:
+                     merge_two_levels: bool = False, fp8_two_pass_p2: bool = False) -> None:
         """Tensor-core schedule: one persistent kernel for the whole neck, or per-level
         kernels on several streams (default) or, with ``single_stream``, one after the other
         on the caller's stream (bitwise the same results as the default).
@@ -304,11 +304,15 @@ class UnifiedFPN:
         results, less launch latency).  ``chain_priority`` (16-bit split schedule): the
         main-stream chain gets the device's highest launch priority.  ``merge_two_levels``:
         the P4 and P3 top-down merges in one launch (when the maps upsample; set it before
-        the first forward of a geometry)."""
+        the first forward of a geometry).  ``fp8_two_pass_p2`` (e4m3 inputs): the P2 lateral
+        runs an absmax pass and then stores M2 as e4m3 itself, instead of storing bf16 M2 for
+        a separate quantisation pass (bitwise the same results; slower at the 640x640 batch-16
+        workload, so off by default)."""
         mode = 1 if fused_neck_kernel else (2 if single_stream else 0)
         check(lib.ufpn_core_set_schedule(self._h, mode), "set_schedule")
         check(lib.ufpn_core_set_schedule_options(self._h, int(programmatic_launch), int(chain_priority),
                                                  int(merge_two_levels)), "set_schedule_options")
+        check(lib.ufpn_core_set_fp8_options(self._h, int(fp8_two_pass_p2)), "set_fp8_options")
 
     def neck_timeline(self, backbone_features) -> dict:
         """Runs one forward with the fused neck kernel's device timeline recorded and

@@ -139,6 +139,12 @@ struct FPNKernelConfig {
   // reference's engine passes 0.01) or SWISH (v / (1 + exp(-v))).
   FPNActivation activation = FPNActivation::NONE;
   float activation_alpha = 0.01f;
+  // e4m3 schedule: the P2 lateral runs twice -- once publishing only the per-image absmax of
+  // its bf16-rounded output, once storing that output quantised to e4m3 -- instead of
+  // storing bf16 M2 for a separate quantisation pass (same codes and scales).  Off: the
+  // lateral is bound by its per-tile epilogue latency, not HBM, so the second pass costs
+  // nearly a whole lateral (R50 640x640 batch 16: 30.3k against 32.4k images/s).
+  bool fp8_two_pass_p2 = false;
   bool enable_graph_capture = true;  // replay the P5->P2 schedule as one CUDA graph
   // Tensor-core path: run all 4 laterals and 4 3x3 convs as ONE persistent kernel with
   // device-side level dependencies (true), or as 8 kernels on two streams (false, the

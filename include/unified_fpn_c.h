@@ -81,6 +81,10 @@ int ufpn_core_set_kernel_config(ufpn_core* core, int tile_size, int channels_per
  * sets the activation with alpha unchanged, 0.01 by default as the reference's engine passes at
  * fpn_engine.cu:356-358); 0 none, 1 ReLU, 2 LeakyReLU, 3 Swish. */
 int ufpn_core_set_activation(ufpn_core* core, int activation, float alpha);
+/* e4m3 schedule: two_pass_p2 = 1 runs the P2 lateral twice (per-image absmax, then the e4m3
+ * store) instead of storing bf16 M2 and quantising it in a separate pass (0, the default:
+ * measured faster); the same codes and scales either way. */
+int ufpn_core_set_fp8_options(ufpn_core* core, int two_pass_p2);
 /* Host-side BatchNorm folding into a conv: for each output channel o, s = gamma[o] /
  * sqrt(var[o] + eps), out_w[o][k] = conv_w[o][k] * s, out_b[o] = (conv_b[o] - mean[o]) * s +
  * beta[o] (conv_b, gamma, beta may be NULL: 0, 1, 0), so conv(out_w, out_b) equals

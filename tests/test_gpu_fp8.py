@@ -263,3 +263,21 @@ def test_fp8_neck_activation(cuda_device):
     ref = O.fpn_neck_e4m3(qf, sc, O.quantize_neck_weights(wts), act="leaky_relu", alpha=0.1)
     for o, r in zip(outs, ref):
         assert O.rel_err(o.float().cpu(), r) < TOL8
+
+
+@pytest.mark.parametrize("geom", [(2, O.R50_CHANNELS, O.level_sizes(128, 192)),
+                                  (16, O.R50_CHANNELS, O.level_sizes(640, 640))])
+def test_fp8_two_pass_p2_lateral_is_bitwise_equal(cuda_device, geom):
+    """The P2 lateral's absmax pass + quantised store against storing bf16 M2 and quantising it
+    in a separate pass (the default): the same e4m3 codes and scales, so bitwise the same
+    outputs; at the benchmark's 640x640 batch-16 size too."""
+    import unified_fpn as U
+    batch, chans, sizes = geom
+    feats, wts, qf, sc = _fp8_case(batch, chans, sizes, seed=41)
+    outs = {}
+    for two_pass in (False, True):
+        fpn = U.UnifiedFPN()
+        fpn.set_schedule(fp8_two_pass_p2=two_pass)
+        _, _, outs[two_pass] = _run_fp8_neck(chans, wts, qf, sc, fpn=fpn)
+    for a, b in zip(outs[False], outs[True]):
+        assert torch.equal(a, b)
