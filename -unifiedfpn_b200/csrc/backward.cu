@@ -40,11 +40,13 @@ namespace {
 constexpr int kDwStages = 3;
 constexpr int kDwChunk = 64 * 128;         // one 64-channel x 64-pixel box, 16-bit: 8 KB
 constexpr int kDwAStage = 4 * kDwChunk;    // 256 output channels (two M = 128 operands)
+constexpr int kDwStaging = 32 * 128;       // epilogue: one 32 x 32 fp32 block (4 KB)
 constexpr int kDwBStage = 4 * kDwChunk;    // 256 input channels
 constexpr int kDwOffB = kDwStages * kDwAStage;
 constexpr int kDwOffBars = kDwOffB + kDwStages * kDwBStage;
 constexpr int kDwSmemBytes = kDwOffBars + 256 + 1024;
 static_assert(kDwSmemBytes <= 232448, "dW smem");
+static_assert(8 * 2 * kDwStaging <= kDwStages * kDwAStage, "epilogue staging reuses the A stages");
 constexpr int kDevTimeoutDw = 0x106;
 
 struct DwArgs {
@@ -59,7 +61,8 @@ struct DwArgs {
 template <typename T>
 __global__ void __launch_bounds__(kTcThreads, 1)
     fpn_dw_gemm_kernel(const __grid_constant__ CUtensorMap map_g,
-                       const __grid_constant__ CUtensorMap map_x, const DwArgs a) {
+                       const __grid_constant__ CUtensorMap map_x,
+                       const __grid_constant__ CUtensorMap map_p, const DwArgs a) {
   constexpr int S = kDwStages;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -98,6 +101,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     fence_barrier_init();
     prefetch_tmap(&map_g);
     prefetch_tmap(&map_x);
+    prefetch_tmap(&map_p);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 2 * kTcBlockN);
@@ -179,36 +183,47 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else {
     // epilogue: accumulator `half` (output channels half*128..), TMEM lane = output channel,
-    // column = input channel; fp32 partial rows
+    // column = input channel.  Each 32 x 32 fp32 block of partial rows is staged in shared
+    // memory (the operand stages are idle once the accumulator is final; 128-byte swizzle:
+    // 16-byte chunk j of row r at j ^ (r & 7)) and stored by one TMA store, two staging
+    // buffers per warp.
+    const int ew = warp - 2;
     const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;
-    const int o = half * 128 + quarter * 32 + lane;
+    const int half = ew >> 2;
+    const int row0 = (split * a.taps + tap) * 256 + half * 128 + quarter * 32;
     const bool ok = mbar_wait(accf_bar, 0, abort_flag, a.status, kDevTimeoutDw);
     if (__all_sync(0xffffffffu, ok)) {
       tc_fence_after();
-      float* row = a.partial +
-                   ((static_cast<size_t>(split) * a.taps + tap) * 256 + o) * a.Cin;
+      uint8_t* const stage = smem + ew * 2 * kDwStaging;
 #pragma unroll 1
       for (int h = 0; h < 8; ++h) {
         const int col = h * 32;
+        const int c0 = cb * 256 + col;
+        if (c0 >= a.Cin) break;  // (the map clips a block that ends beyond Cin)
         uint32_t v[32];
         tmem_ld32(tmem_base + static_cast<uint32_t>(half * kTcBlockN + col) +
                       (static_cast<uint32_t>(quarter * 32) << 16),
                   v);
         tmem_wait_ld();
-        const int c0 = cb * 256 + col;
-        if (c0 + 32 <= a.Cin && (a.Cin & 3) == 0) {
+        uint8_t* buf = stage + (h & 1) * kDwStaging;
+        if (h >= 2) {
+          if (lane == 0) bulk_wait_group_read<1>();  // this buffer's previous store read it
+          __syncwarp();
+        }
+        const uint32_t base = smem_u32(buf) + lane * 128;
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            reinterpret_cast<float4*>(row + c0)[i] =
-                make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
-                            __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (c0 + i < a.Cin) row[c0 + i] = __uint_as_float(v[i]);
+        for (int j = 0; j < 8; ++j)
+          st_shared_v4(base + ((j ^ (lane & 7)) << 4),
+                       make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&map_p, buf, c0, row0);
+          bulk_commit_group();
         }
       }
+      if (lane == 0) bulk_wait_group<0>();
+      __syncwarp();
     }
   }
 
@@ -776,10 +791,13 @@ cudaError_t launch_dw_gemm(DType dt, const void* grad_out, const void* x, int N,
   a.status = status;
   if (static_cast<size_t>(a.ksplit) * taps * 256 * Cin * sizeof(float) > ws_bytes)
     return cudaErrorInvalidValue;
-  CUtensorMap map_g, map_x;
+  CUtensorMap map_g, map_x, map_p;
   cudaError_t e = encode_nhwc_map(&map_g, dt, grad_out, N, H, W, 256, 256, a.kw, a.kh);
   if (e != cudaSuccess) return e;
   if ((e = encode_nhwc_map(&map_x, dt, x, N, H, W, Cin, Cin, a.kw, a.kh)) != cudaSuccess) return e;
+  if ((e = encode_rows_map(&map_p, DType::F32, workspace, Cin,
+                           static_cast<long long>(a.ksplit) * taps * 256, 32, 32)) != cudaSuccess)
+    return e;
   static bool configured[2][64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -793,7 +811,7 @@ cudaError_t launch_dw_gemm(DType dt, const void* grad_out, const void* x, int N,
   }
   const int grid = units * a.ksplit;
   e = launch_ex(kern, dim3(grid), dim3(kTcThreads), kDwSmemBytes, s, LaunchOpts(), 1, map_g, map_x,
-                a);
+                map_p, a);
   if (e != cudaSuccess) return e;
   const long long per = static_cast<long long>(taps) * 256 * Cin;
   return launch_ex(reduce_partials_kernel, dim3(grid_for(per, 256)), dim3(256), 0, s, LaunchOpts(),

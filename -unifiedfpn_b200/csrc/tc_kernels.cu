@@ -38,6 +38,8 @@ CUtensorMapDataType tmap_dtype(DType dt) {
       return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     case DType::BF16:
       return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    case DType::F32:
+      return CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
     default:
       return CU_TENSOR_MAP_DATA_TYPE_UINT8;
   }
@@ -452,6 +454,16 @@ cudaError_t encode_nhwc_map(CUtensorMap* map, DType dt, const void* base, int N,
   uint32_t box[4] = {static_cast<uint32_t>(128 / esz), static_cast<uint32_t>(bw),
                      static_cast<uint32_t>(bh), 1};
   return encode(map, dt, 4, base, dims, strides, box);
+}
+
+cudaError_t encode_rows_map(CUtensorMap* map, DType dt, const void* base, int cols, long long rows,
+                            int box_cols, int box_rows) {
+  if (cols <= 0 || rows <= 0 || box_cols * dtype_size(dt) != 128) return cudaErrorInvalidValue;
+  const uint64_t esz = static_cast<uint64_t>(dtype_size(dt));
+  uint64_t dims[2] = {static_cast<uint64_t>(cols), static_cast<uint64_t>(rows)};
+  uint64_t strides[1] = {static_cast<uint64_t>(cols) * esz};
+  uint32_t box[2] = {static_cast<uint32_t>(box_cols), static_cast<uint32_t>(box_rows)};
+  return encode(map, dt, 2, base, dims, strides, box);
 }
 
 cudaError_t tc_set_output_view(TcPlan& plan, void* out, int C, int pix_stride) {

@@ -210,6 +210,10 @@ cudaError_t encode_nhwc_map(CUtensorMap* map, DType dt, const void* base, int N,
 // pix_stride elements apart (out = that channel slice's first element).  Used to write the
 // 256-channel slices of a wider tensor (the input gradient of a Cin > 256 lateral).
 cudaError_t tc_set_output_view(TcPlan& plan, void* out, int C, int pix_stride);
+// Row-major [rows][cols] map with a (box_cols, box_rows) box whose inner extent is one
+// 128-byte row (128-byte swizzle): row tiles staged in shared memory, stored by TMA.
+cudaError_t encode_rows_map(CUtensorMap* map, DType dt, const void* base, int cols, long long rows,
+                            int box_cols, int box_rows);
 // One launch of a 16-bit lateral plan (no top-down add, plain output) for `slices` output
 // channel slices of 256: weights w [slices * 256][K] row-major (K = the plan's input
 // channels), bias [slices * 256], output NHWC with C channels (256 (slices - 1) < C <= 256
