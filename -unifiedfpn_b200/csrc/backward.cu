@@ -55,8 +55,15 @@ struct DwArgs {
   int c_blocks, taps;
   int Cin;
   float* partial;  // [ksplit][taps][256][Cin]
+  // bias gradient partials [ksplit][taps][256] (null: none): the idle epilogue warps of the
+  // channel-block-0 CTAs also sum dY (plain loads of g, NHWC [N][H][W][256], mostly L2 hits
+  // behind the operand TMA), the CTA of tap t over every taps-th k-block of its range from t
+  float* db_partial;
+  const void* g;
+  int H, W;
   int* status;
 };
+constexpr int kDwEpiWarps = 8;  // warps 2..9
 
 template <typename T>
 __global__ void __launch_bounds__(kTcThreads, 1)
@@ -89,6 +96,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int dx = a.taps == 9 ? tap % 3 - 1 : 0;
   const int kb0 = split * a.per_kb;
   const int kb1 = min(a.num_kb, kb0 + a.per_kb);  // non-empty (host)
+  // bias-gradient CTA: its epilogue warps sum dY over its share of the pixel range meanwhile
+  const bool do_db = a.db_partial != nullptr && cb == 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -191,7 +200,59 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int quarter = warp & 3;
     const int half = ew >> 2;
     const int row0 = (split * a.taps + tap) * 256 + half * 128 + quarter * 32;
+    float db[8];
+    if (do_db) {
+      // thread e sums 16-byte group g16 (channels 8 g16 ..) of box pixels rl, rl + 8, ..,
+      // rl + 56 of k-blocks kb0 + tap, kb0 + tap + taps, .. (the boxes the producer loads),
+      // two k-blocks' loads in flight
+      const int e = ew * 32 + lane;
+      const int g16 = e & 31, rl = e >> 5;
+      const uint4* gp = reinterpret_cast<const uint4*>(a.g) + g16;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) db[i] = 0.f;
+      for (int kb = kb0 + tap; kb < kb1; kb += 2 * a.taps) {
+        uint4 u[16];
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+          const int k2 = kb + b * a.taps;
+          const int tx = k2 % a.tiles_x;
+          const int t2 = k2 / a.tiles_x;
+          const int ty = t2 % a.tiles_y;
+          const int n = t2 / a.tiles_y;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int p = rl + 8 * k;
+            const int x = tx * a.kw + p % a.kw, y = ty * a.kh + p / a.kw;
+            u[8 * b + k] = make_uint4(0u, 0u, 0u, 0u);
+            if (k2 < kb1 && x < a.W && y < a.H)
+              u[8 * b + k] = __ldg(gp + ((static_cast<size_t>(n) * a.H + y) * a.W + x) * 32);
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          const uint32_t w4[4] = {u[k].x, u[k].y, u[k].z, u[k].w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = Pack<T>::unpack(w4[i]);
+            db[2 * i] += f.x;
+            db[2 * i + 1] += f.y;
+          }
+        }
+      }
+    }
     const bool ok = mbar_wait(accf_bar, 0, abort_flag, a.status, kDevTimeoutDw);
+    if (do_db) {
+      // every MMA is done: the B stages are free for the fixed-order sum of the 8 row lanes
+      float* red = reinterpret_cast<float*>(smem_b);
+      const int e = ew * 32 + lane;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) red[(e >> 5) * 256 + (e & 31) * 8 + i] = db[i];
+      asm volatile("bar.sync 1, %0;" ::"n"(kDwEpiWarps * 32) : "memory");
+      float acc = 0.f;
+      for (int r = 0; r < 8; ++r) acc += red[r * 256 + e];
+      if (__all_sync(0xffffffffu, ok))
+        a.db_partial[(static_cast<size_t>(split) * a.taps + tap) * 256 + e] = acc;
+    }
     if (__all_sync(0xffffffffu, ok)) {
       tc_fence_after();
       uint8_t* const stage = smem + ew * 2 * kDwStaging;
@@ -239,12 +300,34 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 // out[(o * taps + t) * Cin + c] = sum over s of partial[s][t][o][c], in a fixed order: four
 // running sums over s = 0, 4, 8, .. / 1, 5, 9, .. / .., added last (four loads in flight per
 // thread instead of one dependent chain of ksplit loads)
+// (With grad_b: indices per .. per + 255 sum the db_rows rows db_partial[r][o] the same way
+// into grad_b[o].)
 __global__ void __launch_bounds__(256) reduce_partials_kernel(const float* __restrict__ partial,
                                                               float* __restrict__ out, int ksplit,
-                                                              int taps, int Cin) {
+                                                              int taps, int Cin,
+                                                              const float* __restrict__ db_partial,
+                                                              float* __restrict__ grad_b,
+                                                              int db_rows) {
   const long long per = static_cast<long long>(taps) * 256 * Cin;
-  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < per;
+  const long long total = per + (grad_b ? 256 : 0);
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    if (i >= per) {
+      const int o = static_cast<int>(i - per);
+      float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
+      int s = 0;
+      for (; s + 4 <= db_rows; s += 4) {
+        b0 += __ldg(db_partial + s * 256 + o);
+        b1 += __ldg(db_partial + (s + 1) * 256 + o);
+        b2 += __ldg(db_partial + (s + 2) * 256 + o);
+        b3 += __ldg(db_partial + (s + 3) * 256 + o);
+      }
+      if (s < db_rows) b0 += __ldg(db_partial + s * 256 + o);
+      if (s + 1 < db_rows) b1 += __ldg(db_partial + (s + 1) * 256 + o);
+      if (s + 2 < db_rows) b2 += __ldg(db_partial + (s + 2) * 256 + o);
+      grad_b[o] = (b0 + b1) + (b2 + b3);
+      continue;
+    }
     float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
     int s = 0;
     for (; s + 4 <= ksplit; s += 4) {
@@ -765,12 +848,13 @@ size_t dw_gemm_workspace_bytes(int N, int H, int W, int Cin, int taps) {
   const int units = taps * ((Cin + 255) / 256);
   int per = 1, ksplit = 1;
   dw_split(num_kb, units, per, ksplit);
-  return static_cast<size_t>(ksplit) * taps * 256 * Cin * sizeof(float);
+  // weight partials, then the bias partials [ksplit][taps][256]
+  return static_cast<size_t>(ksplit) * taps * (static_cast<size_t>(256) * Cin + 256) * sizeof(float);
 }
 
 cudaError_t launch_dw_gemm(DType dt, const void* grad_out, const void* x, int N, int H, int W,
-                           int Cin, int taps, float* grad_w, float* workspace, size_t ws_bytes,
-                           int* status, cudaStream_t s) {
+                           int Cin, int taps, float* grad_w, float* grad_b, float* workspace,
+                           size_t ws_bytes, int* status, cudaStream_t s) {
   if (dt != DType::BF16 && dt != DType::F16) return cudaErrorNotSupported;
   if (N <= 0 || H <= 0 || W <= 0 || Cin <= 0 || Cin % 8 != 0 || (taps != 1 && taps != 9))
     return cudaErrorInvalidValue;
@@ -789,8 +873,13 @@ cudaError_t launch_dw_gemm(DType dt, const void* grad_out, const void* x, int N,
   dw_split(a.num_kb, units, a.per_kb, a.ksplit);
   a.partial = workspace;
   a.status = status;
-  if (static_cast<size_t>(a.ksplit) * taps * 256 * Cin * sizeof(float) > ws_bytes)
+  const size_t wparts = static_cast<size_t>(a.ksplit) * taps * 256 * Cin;
+  if ((wparts + static_cast<size_t>(a.ksplit) * taps * 256) * sizeof(float) > ws_bytes)
     return cudaErrorInvalidValue;
+  a.db_partial = grad_b ? workspace + wparts : nullptr;
+  a.g = grad_out;
+  a.H = H;
+  a.W = W;
   CUtensorMap map_g, map_x, map_p;
   cudaError_t e = encode_nhwc_map(&map_g, dt, grad_out, N, H, W, 256, 256, a.kw, a.kh);
   if (e != cudaSuccess) return e;
@@ -813,9 +902,10 @@ cudaError_t launch_dw_gemm(DType dt, const void* grad_out, const void* x, int N,
   e = launch_ex(kern, dim3(grid), dim3(kTcThreads), kDwSmemBytes, s, LaunchOpts(), 1, map_g, map_x,
                 map_p, a);
   if (e != cudaSuccess) return e;
-  const long long per = static_cast<long long>(taps) * 256 * Cin;
+  const long long per = static_cast<long long>(taps) * 256 * Cin + (grad_b ? 256 : 0);
   return launch_ex(reduce_partials_kernel, dim3(grid_for(per, 256)), dim3(256), 0, s, LaunchOpts(),
-                   1, static_cast<const float*>(workspace), grad_w, a.ksplit, taps, Cin);
+                   1, static_cast<const float*>(workspace), grad_w, a.ksplit, taps, Cin,
+                   static_cast<const float*>(a.db_partial), grad_b, a.ksplit * taps);
 }
 
 // Column sums: at most 4 blocks per SM (all resident at once), each over a contiguous run of at

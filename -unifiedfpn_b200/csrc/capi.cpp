@@ -535,7 +535,8 @@ int ufpn_lateral_conv_backward(int dtype, const void* x, const void* w, const vo
   const size_t wt_bytes = grad_x ? static_cast<size_t>(cblk) * 256 * 256 * esz : 0;
   const size_t zb_bytes = static_cast<size_t>(cblk) * 256 * sizeof(float);  // zero bias of dX
   const size_t dw_bytes = grad_w ? ufpn::dw_gemm_workspace_bytes(N, H, W, Cin, 1) : 0;
-  const size_t cs_bytes = grad_b ? ufpn::colsum_workspace_bytes(pixels, 256) : 0;
+  // (the bias gradient comes out of the weight-gradient launch when both are asked for)
+  const size_t cs_bytes = grad_b && !grad_w ? ufpn::colsum_workspace_bytes(pixels, 256) : 0;
   StreamScratch scratch(s);
   cudaError_t e = scratch.alloc(wt_bytes + zb_bytes + dw_bytes + cs_bytes);
   if (e != cudaSuccess) return cuda_fail(e, "backward scratch");
@@ -557,11 +558,11 @@ int ufpn_lateral_conv_backward(int dtype, const void* x, const void* w, const vo
   }
   if (grad_w) {
     float* ws = reinterpret_cast<float*>(base + wt_bytes + zb_bytes);
-    e = ufpn::launch_dw_gemm(dt, grad_out, x, N, H, W, Cin, 1, grad_w, ws, dw_bytes,
+    e = ufpn::launch_dw_gemm(dt, grad_out, x, N, H, W, Cin, 1, grad_w, grad_b, ws, dw_bytes,
                              device_status_word(), s);
     if (e != cudaSuccess) return cuda_fail(e, "lateral weight gradient");
   }
-  if (grad_b) {
+  if (grad_b && !grad_w) {
     float* ws = reinterpret_cast<float*>(base + wt_bytes + zb_bytes + dw_bytes);
     e = ufpn::launch_colsum(dt, grad_out, pixels, 256, grad_b, ws, cs_bytes, s);
     if (e != cudaSuccess) return cuda_fail(e, "bias gradient");
@@ -586,7 +587,8 @@ int ufpn_conv3x3_backward(int dtype, const void* x, const void* w, const void* g
   const size_t wf_bytes = grad_x ? 256ull * 9 * 256 * esz : 0;
   const size_t zb_bytes = 1024;
   const size_t dw_bytes = grad_w ? ufpn::dw_gemm_workspace_bytes(N, H, W, 256, 9) : 0;
-  const size_t cs_bytes = grad_b ? ufpn::colsum_workspace_bytes(pixels, 256) : 0;
+  // (the bias gradient comes out of the weight-gradient launch when both are asked for)
+  const size_t cs_bytes = grad_b && !grad_w ? ufpn::colsum_workspace_bytes(pixels, 256) : 0;
   StreamScratch scratch(s);
   cudaError_t e = scratch.alloc(wf_bytes + zb_bytes + dw_bytes + cs_bytes);
   if (e != cudaSuccess) return cuda_fail(e, "backward scratch");
@@ -604,11 +606,11 @@ int ufpn_conv3x3_backward(int dtype, const void* x, const void* w, const void* g
   }
   if (grad_w) {
     float* ws = reinterpret_cast<float*>(base + wf_bytes + zb_bytes);
-    e = ufpn::launch_dw_gemm(dt, grad_out, x, N, H, W, 256, 9, grad_w, ws, dw_bytes,
+    e = ufpn::launch_dw_gemm(dt, grad_out, x, N, H, W, 256, 9, grad_w, grad_b, ws, dw_bytes,
                              device_status_word(), s);
     if (e != cudaSuccess) return cuda_fail(e, "3x3 weight gradient");
   }
-  if (grad_b) {
+  if (grad_b && !grad_w) {
     float* ws = reinterpret_cast<float*>(base + wf_bytes + zb_bytes + dw_bytes);
     e = ufpn::launch_colsum(dt, grad_out, pixels, 256, grad_b, ws, cs_bytes, s);
     if (e != cudaSuccess) return cuda_fail(e, "bias gradient");

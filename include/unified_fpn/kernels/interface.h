@@ -271,9 +271,11 @@ cudaError_t launch_tc(const TcPlan& plan, cudaStream_t s, LaunchOpts opts = Laun
 // NHWC dY [N][H][W][256] and X [N][H][W][Cin] (16-bit): a tensor-core GEMM over pixels with
 // fp32 split-K partials in `workspace` (dw_gemm_workspace_bytes) added in a fixed order.
 size_t dw_gemm_workspace_bytes(int N, int H, int W, int Cin, int taps);
+// With grad_b (nullable), grad_b[o] = sum_p dY[p][o] comes out of the same launch: one unit's
+// CTAs also sum the dY tiles they stream (fixed-order partials, reduced with dW).
 cudaError_t launch_dw_gemm(DType dt, const void* grad_out, const void* x, int N, int H, int W,
-                           int Cin, int taps, float* grad_w, float* workspace, size_t ws_bytes,
-                           int* status, cudaStream_t s);
+                           int Cin, int taps, float* grad_w, float* grad_b, float* workspace,
+                           size_t ws_bytes, int* status, cudaStream_t s);
 // out[c] = sum over the pixels of g[p][c] (fp32; per block, then in a fixed order).
 size_t colsum_workspace_bytes(long long pixels, int C);
 cudaError_t launch_colsum(DType dt, const void* g, long long pixels, int C, float* out,

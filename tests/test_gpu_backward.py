@@ -149,3 +149,35 @@ def test_backward_is_deterministic(cuda_device):
         assert torch.equal(p, q)
     up = [U.fpn_upsample_add_backward(gy, (20, 28)) for _ in range(2)]
     assert torch.equal(up[0], up[1])
+
+
+@pytest.mark.parametrize("taps", [1, 9])
+def test_bias_gradient_alone_and_with_weights(cuda_device, taps):
+    """grad_b with grad_w (summed inside the weight-gradient launch) and grad_b alone (the
+    column-sum kernels) both equal the sum of dY over its pixels."""
+    import unified_fpn as U
+    from unified_fpn import _lib
+    g = torch.Generator().manual_seed(11 + taps)
+    n, h, w = 2, 23, 37
+    x = _cl(torch.randn(n, 256, h, w, generator=g).to(torch.bfloat16).to(cuda_device))
+    gy = _cl(torch.randn(n, 256, h, w, generator=g).to(torch.bfloat16).to(cuda_device))
+    ref = gy.float().sum(dim=(0, 2, 3)).cpu()
+    if taps == 1:
+        wt = (torch.randn(256, 256, generator=g) * 0.05).to(torch.bfloat16).to(cuda_device)
+        _, _, gb_fused = U.fpn_lateral_conv_backward(x, wt, gy)
+    else:
+        wt = U.pack_conv3x3_weight((torch.randn(256, 256, 3, 3, generator=g) * 0.03).to(cuda_device),
+                                   torch.bfloat16)
+        _, _, gb_fused = U.fpn_conv3x3_backward(x, wt, gy)
+    gb_alone = torch.zeros(256, device=cuda_device)
+    stream = torch.cuda.current_stream().cuda_stream
+    if taps == 1:
+        rc = _lib.lib.ufpn_lateral_conv_backward(_lib.DTYPE_BF16, x.data_ptr(), wt.data_ptr(), gy.data_ptr(),
+                                                 None, None, gb_alone.data_ptr(), n, 256, h, w, stream)
+    else:
+        rc = _lib.lib.ufpn_conv3x3_backward(_lib.DTYPE_BF16, x.data_ptr(), wt.data_ptr(), gy.data_ptr(),
+                                            None, None, gb_alone.data_ptr(), n, h, w, stream)
+    torch.cuda.synchronize()
+    assert rc == 0 and U.device_status() == 0
+    for gb in (gb_fused, gb_alone):
+        assert O.rel_err(gb.cpu(), ref) < 1e-5
