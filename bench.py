@@ -239,6 +239,13 @@ def run_train(args, rank, world, local, dev):
                       .contiguous(memory_format=torch.channels_last) for h, w in out_sizes])
     in_mb = sum(B * c * h * w * 2 for c, (h, w) in zip(R50_CHANNELS, sizes)) / 1e6
     neck = U.FPNNeck(R50_CHANNELS).to(dev)
+    # graphs read their captured input buffers: each step copies its set into them (on the
+    # device, inside the timed region, 117 MB per step)
+    run = neck
+    static = None
+    if args.graph:
+        static = [f.detach().clone().requires_grad_() for f in feats[0]]
+        run = neck.make_graphed(static)
 
     def step(i):
         k = i % n_sets
@@ -246,7 +253,13 @@ def run_train(args, rank, world, local, dev):
             p.grad = None
         for f in feats[k]:
             f.grad = None
-        outs = neck(feats[k])
+        if static is not None:
+            with torch.no_grad():
+                for dst, src in zip(static, feats[k]):
+                    dst.copy_(src)
+            outs = run(static)
+        else:
+            outs = run(feats[k])
         torch.autograd.backward(outs, grads[k])
 
     for i in range(args.warmup):
@@ -285,7 +298,9 @@ def run_train(args, rank, world, local, dev):
             "data": "synthetic (seeded N(0,1) after ReLU clamp; seeded N(0,1) output gradients; "
                     "random Kaiming-normal fp32 master weights)",
             "config": {"workload": f"R50 FPN neck training step {args.height}x{args.width}, {B} images/GPU, "
-                                   f"{args.dtype} NHWC, gradients of every input, weight and bias",
+                                   f"{args.dtype} NHWC, gradients of every input, weight and bias"
+                                   + (", replayed as CUDA graphs (inputs copied into the captured "
+                                      "buffers each step)" if args.graph else ""),
                        "global_batch": B * world, "per_gpu_batch": B,
                        "l2": f"inputs rotate over {n_sets} sets ({n_sets} x {in_mb:.0f} MB) > 126 MB L2",
                        "parallelism": f"dp{world} batch shards (gradients not reduced)"},
@@ -325,6 +340,8 @@ def main():
                          "per-level kernels one after the other on one stream")
     ap.add_argument("--train", action="store_true",
                     help="time the training step (FPNNeck forward + backward) instead")
+    ap.add_argument("--graph", action="store_true",
+                    help="with --train: replay the step as CUDA graphs (FPNNeck.make_graphed)")
     args = ap.parse_args()
     if args.train and args.dtype == "e4m3":
         ap.error("--train runs on bf16 or fp16")

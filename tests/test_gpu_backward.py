@@ -181,3 +181,36 @@ def test_bias_gradient_alone_and_with_weights(cuda_device, taps):
     assert rc == 0 and U.device_status() == 0
     for gb in (gb_fused, gb_alone):
         assert O.rel_err(gb.cpu(), ref) < 1e-5
+
+
+def test_graphed_training_step_matches_eager(cuda_device):
+    """FPNNeck.make_graphed: forward and backward replayed as CUDA graphs give bitwise the
+    outputs and gradients of the eager step, also after the weights change."""
+    import unified_fpn as U
+    sizes = O.level_sizes(128, 160)
+    fs = O.make_features(2, O.R50_CHANNELS, sizes, seed=51, dist="normal")
+    neck = U.FPNNeck(O.R50_CHANNELS).to(cuda_device)
+    feats = [_cl(f.to(torch.bfloat16).to(cuda_device)).requires_grad_() for f in fs]
+    g = torch.Generator().manual_seed(52)
+    with torch.no_grad():
+        shapes = [o.shape for o in neck([f.detach() for f in feats])]
+    grads = [_cl(torch.randn(s, generator=g).to(torch.bfloat16).to(cuda_device)) for s in shapes]
+    # (no eager autograd graph may be alive while the graphs are captured)
+    run = neck.make_graphed([f.detach().clone().requires_grad_() for f in feats])
+    for it in range(2):
+        results = []
+        for fn in (neck, run):
+            for p in neck.parameters():
+                p.grad = None
+            for f in feats:
+                f.grad = None
+            outs = fn(feats)
+            torch.autograd.backward(outs, grads)
+            torch.cuda.synchronize()
+            results.append([o.detach().clone() for o in outs] + [p.grad.clone() for p in neck.parameters()]
+                           + [f.grad.clone() for f in feats])
+        assert all(torch.equal(a, b) for a, b in zip(*results))
+        with torch.no_grad():  # an optimiser step: the graphs read the weights in place
+            for p in neck.parameters():
+                p.mul_(0.5)
+    assert U.device_status() == 0
