@@ -297,7 +297,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 }
 
-// out[(o * taps + t) * Cin + c] = sum over s of partial[s][t][o][c], in a fixed order: four
+// out[(o * Cin + c) * taps + t] = sum over s of partial[s][t][o][c] (for the 3x3 the
+// [256][256][3][3] order of its fp32 weights), in a fixed order: four
 // running sums over s = 0, 4, 8, .. / 1, 5, 9, .. / .., added last (four loads in flight per
 // thread instead of one dependent chain of ksplit loads)
 // (With grad_b: indices per .. per + 255 sum the db_rows rows db_partial[r][o] the same way
@@ -344,7 +345,7 @@ __global__ void __launch_bounds__(256) reduce_partials_kernel(const float* __res
     const long long to = i / Cin;
     const int o = static_cast<int>(to % 256);
     const int t = static_cast<int>(to / 256);
-    out[(static_cast<size_t>(o) * taps + t) * Cin + c] = acc;
+    out[(static_cast<size_t>(o) * Cin + c) * taps + t] = acc;  // [o][c][ky][kx] (taps 9)
   }
 }
 
@@ -783,6 +784,55 @@ __global__ void __launch_bounds__(256) p6_adjoint_kernel(const T* __restrict__ g
 }
 
 // ------------------------------------------------------------------ weight layouts
+constexpr int kPrepMaxJobs = 16;
+struct PrepArgs {
+  long long begin[kPrepMaxJobs + 1];  // flat element range of job j: [begin[j], begin[j + 1])
+  const float* in[kPrepMaxJobs];
+  void* out[kPrepMaxJobs];
+  int kind[kPrepMaxJobs];
+  int cin[kPrepMaxJobs];
+  int num_jobs;
+};
+
+// Every output element of every job (WeightPrepJob kinds), one launch, writes coalesced.
+template <typename T>
+__global__ void __launch_bounds__(256) prepare_weights_kernel(const __grid_constant__ PrepArgs a) {
+  const long long total = a.begin[a.num_jobs];
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    int j = 0;
+    while (j + 1 < a.num_jobs && i >= a.begin[j + 1]) ++j;
+    const long long k = i - a.begin[j];
+    const float* in = a.in[j];
+    const int cin = a.cin[j];
+    float v;
+    switch (a.kind[j]) {
+      case 0:  // [o][c]
+        v = in[k];
+        break;
+      case 1: {  // [c][o] <- [o][c], zero rows c >= cin
+        const int c = static_cast<int>(k >> 8), o = static_cast<int>(k & 255);
+        v = c < cin ? in[static_cast<size_t>(o) * cin + c] : 0.f;
+        break;
+      }
+      case 2: {  // [o][t][c] <- [o][c][t]
+        const int c = static_cast<int>(k & 255);
+        const int t = static_cast<int>((k >> 8) % 9);
+        const int o = static_cast<int>(k / 2304);
+        v = in[(static_cast<size_t>(o) * 256 + c) * 9 + t];
+        break;
+      }
+      default: {  // [c][t][o] <- [o][c][8 - t]
+        const int o = static_cast<int>(k & 255);
+        const int t = static_cast<int>((k >> 8) % 9);
+        const int c = static_cast<int>(k / 2304);
+        v = in[(static_cast<size_t>(o) * 256 + c) * 9 + (8 - t)];
+        break;
+      }
+    }
+    static_cast<T*>(a.out[j])[k] = bw_from_f<T>(v);
+  }
+}
 // out[c][r] = in[r][c] for an R x C matrix (rows of out beyond C up to out_rows are zeroed)
 template <typename T>
 __global__ void __launch_bounds__(256) transpose_kernel(const T* __restrict__ in, T* __restrict__ out,
@@ -966,6 +1016,38 @@ cudaError_t launch_staged_adjoint(K kernel, long long blocks, size_t smem, cudaS
   }
   return launch_ex(kernel, dim3(static_cast<unsigned>(blocks)), dim3(kUaThreads), smem, s,
                    LaunchOpts(), 1, args...);
+}
+
+cudaError_t launch_prepare_weights(DType dt, const WeightPrepJob* jobs, int num_jobs,
+                                   cudaStream_t s) {
+  if (num_jobs < 1 || num_jobs > kPrepMaxJobs || !jobs) return cudaErrorInvalidValue;
+  PrepArgs a;
+  std::memset(&a, 0, sizeof(a));
+  long long at = 0;
+  for (int j = 0; j < num_jobs; ++j) {
+    const WeightPrepJob& jb = jobs[j];
+    if (!jb.in || !jb.out || jb.kind < 0 || jb.kind > 3 || jb.cin <= 0) return cudaErrorInvalidValue;
+    a.begin[j] = at;
+    a.in[j] = jb.in;
+    a.out[j] = jb.out;
+    a.kind[j] = jb.kind;
+    a.cin[j] = jb.cin;
+    const long long cblk = (jb.cin + 255) / 256;
+    at += jb.kind == 0 ? 256LL * jb.cin : jb.kind == 1 ? cblk * 256 * 256 : 256LL * 9 * 256;
+  }
+  a.begin[num_jobs] = at;
+  a.num_jobs = num_jobs;
+  const unsigned grid = grid_for(at, 256);
+  switch (dt) {
+    case DType::BF16:
+      return launch_ex(prepare_weights_kernel<__nv_bfloat16>, dim3(grid), dim3(256), 0, s,
+                       LaunchOpts(), 1, a);
+    case DType::F16:
+      return launch_ex(prepare_weights_kernel<__half>, dim3(grid), dim3(256), 0, s, LaunchOpts(),
+                       1, a);
+    default:
+      return cudaErrorNotSupported;
+  }
 }
 
 cudaError_t launch_upsample_adjoint(DType dt, const void* grad_fine, const void* base, void* out,

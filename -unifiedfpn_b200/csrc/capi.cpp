@@ -516,37 +516,61 @@ bool parse_16bit(int dtype, DType* dt) {
 }
 }  // namespace
 
-int ufpn_lateral_conv_backward(int dtype, const void* x, const void* w, const void* grad_out,
-                               void* grad_x, float* grad_w, float* grad_b, int N, int Cin, int H,
-                               int W, void* stream) {
+// Zero fp32 bias of the input-gradient launches (2048 floats, enough for Cin = 2048), one per
+// device, made on first use (outside any stream capture: the first backward call).
+const float* device_zeros() {
+  static float* zeros[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(g_status_mu);
+  if (!zeros[dev]) {
+    float* p = nullptr;
+    if (cudaMalloc(&p, 2048 * sizeof(float)) != cudaSuccess) return nullptr;
+    if (cudaMemset(p, 0, 2048 * sizeof(float)) != cudaSuccess) {
+      cudaFree(p);
+      return nullptr;
+    }
+    zeros[dev] = p;
+  }
+  return zeros[dev];
+}
+
+// Lateral backward; the input gradient uses w_t ([cblk * 256][256], w transposed with zero
+// rows beyond Cin) if given, else transposes w into scratch.
+int lateral_backward(int dtype, const void* x, const void* w, const void* w_t,
+                     const void* grad_out, void* grad_x, float* grad_w, float* grad_b, int N,
+                     int Cin, int H, int W, void* stream) {
   DType dt;
   if (!parse_16bit(dtype, &dt)) return fail(UFPN_ERR_UNSUPPORTED, "backward takes bf16 or fp16");
-  if (!grad_out || (grad_x && !w) || (grad_w && !x))
+  if (!grad_out || (grad_x && !w && !w_t) || (grad_w && !x))
     return fail(UFPN_ERR_INVALID_ARG, "NULL tensor pointer");
   if (N <= 0 || Cin <= 0 || H <= 0 || W <= 0) return fail(UFPN_ERR_INVALID_ARG, "sizes must be positive");
-  if (Cin % 8 != 0) return fail(UFPN_ERR_UNSUPPORTED, "Cin must be a multiple of 8");
+  if (Cin % 8 != 0 || Cin > 2048) return fail(UFPN_ERR_UNSUPPORTED, "Cin must be a multiple of 8, at most 2048");
   if (!ufpn::aligned16(grad_out) || (x && !ufpn::aligned16(x)) || (w && !ufpn::aligned16(w)) ||
-      (grad_x && !ufpn::aligned16(grad_x)))
+      (w_t && !ufpn::aligned16(w_t)) || (grad_x && !ufpn::aligned16(grad_x)))
     return fail(UFPN_ERR_ALIGNMENT, "tensors must be 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const long long pixels = static_cast<long long>(N) * H * W;
   const int cblk = (Cin + 255) / 256;
   const size_t esz = ufpn::dtype_size(dt);
-  const size_t wt_bytes = grad_x ? static_cast<size_t>(cblk) * 256 * 256 * esz : 0;
-  const size_t zb_bytes = static_cast<size_t>(cblk) * 256 * sizeof(float);  // zero bias of dX
+  const size_t wt_bytes = grad_x && !w_t ? static_cast<size_t>(cblk) * 256 * 256 * esz : 0;
   const size_t dw_bytes = grad_w ? ufpn::dw_gemm_workspace_bytes(N, H, W, Cin, 1) : 0;
   // (the bias gradient comes out of the weight-gradient launch when both are asked for)
   const size_t cs_bytes = grad_b && !grad_w ? ufpn::colsum_workspace_bytes(pixels, 256) : 0;
   StreamScratch scratch(s);
-  cudaError_t e = scratch.alloc(wt_bytes + zb_bytes + dw_bytes + cs_bytes);
+  cudaError_t e = scratch.alloc(wt_bytes + dw_bytes + cs_bytes + 16);
   if (e != cudaSuccess) return cuda_fail(e, "backward scratch");
   uint8_t* base = static_cast<uint8_t*>(scratch.p);
   if (grad_x) {
-    void* wt = base;
-    float* zero_bias = reinterpret_cast<float*>(base + wt_bytes);
-    if ((e = cudaMemsetAsync(zero_bias, 0, zb_bytes, s)) != cudaSuccess) return cuda_fail(e, "memset");
-    if ((e = ufpn::launch_transpose_weights(dt, w, wt, 256, Cin, cblk * 256, s)) != cudaSuccess)
-      return cuda_fail(e, "transpose weights");
+    const float* zero_bias = device_zeros();
+    if (!zero_bias) return fail(UFPN_ERR_CUDA, "device zeros");
+    const void* wt = w_t;
+    if (!wt) {
+      if ((e = ufpn::launch_transpose_weights(dt, w, base, 256, Cin, cblk * 256, s)) != cudaSuccess)
+        return cuda_fail(e, "transpose weights");
+      wt = base;
+    }
     // grad_x[:, 256 cb .. +256) = grad_out . w^T[256 cb .. +256) for every slice cb: a
     // 256-channel lateral per slice, all slices in one launch
     ufpn::TcPlan plan;
@@ -557,65 +581,129 @@ int ufpn_lateral_conv_backward(int dtype, const void* x, const void* w, const vo
     if (e != cudaSuccess) return cuda_fail(e, "lateral input gradient");
   }
   if (grad_w) {
-    float* ws = reinterpret_cast<float*>(base + wt_bytes + zb_bytes);
+    float* ws = reinterpret_cast<float*>(base + wt_bytes);
     e = ufpn::launch_dw_gemm(dt, grad_out, x, N, H, W, Cin, 1, grad_w, grad_b, ws, dw_bytes,
                              device_status_word(), s);
     if (e != cudaSuccess) return cuda_fail(e, "lateral weight gradient");
   }
   if (grad_b && !grad_w) {
-    float* ws = reinterpret_cast<float*>(base + wt_bytes + zb_bytes + dw_bytes);
+    float* ws = reinterpret_cast<float*>(base + wt_bytes + dw_bytes);
     e = ufpn::launch_colsum(dt, grad_out, pixels, 256, grad_b, ws, cs_bytes, s);
     if (e != cudaSuccess) return cuda_fail(e, "bias gradient");
   }
   return UFPN_OK;
 }
 
-int ufpn_conv3x3_backward(int dtype, const void* x, const void* w, const void* grad_out,
-                          void* grad_x, float* grad_w, float* grad_b, int N, int H, int W,
-                          void* stream) {
+// 3x3 backward; the input gradient uses w_f ([256 c][9][256 o], the packed weights flipped)
+// if given, else flips w into scratch.
+int conv3x3_backward(int dtype, const void* x, const void* w, const void* w_f,
+                     const void* grad_out, void* grad_x, float* grad_w, float* grad_b, int N,
+                     int H, int W, void* stream) {
   DType dt;
   if (!parse_16bit(dtype, &dt)) return fail(UFPN_ERR_UNSUPPORTED, "backward takes bf16 or fp16");
-  if (!grad_out || (grad_x && !w) || (grad_w && !x))
+  if (!grad_out || (grad_x && !w && !w_f) || (grad_w && !x))
     return fail(UFPN_ERR_INVALID_ARG, "NULL tensor pointer");
   if (N <= 0 || H <= 0 || W <= 0) return fail(UFPN_ERR_INVALID_ARG, "sizes must be positive");
   if (!ufpn::aligned16(grad_out) || (x && !ufpn::aligned16(x)) || (w && !ufpn::aligned16(w)) ||
-      (grad_x && !ufpn::aligned16(grad_x)))
+      (w_f && !ufpn::aligned16(w_f)) || (grad_x && !ufpn::aligned16(grad_x)))
     return fail(UFPN_ERR_ALIGNMENT, "tensors must be 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const long long pixels = static_cast<long long>(N) * H * W;
   const size_t esz = ufpn::dtype_size(dt);
-  const size_t wf_bytes = grad_x ? 256ull * 9 * 256 * esz : 0;
-  const size_t zb_bytes = 1024;
+  const size_t wf_bytes = grad_x && !w_f ? 256ull * 9 * 256 * esz : 0;
   const size_t dw_bytes = grad_w ? ufpn::dw_gemm_workspace_bytes(N, H, W, 256, 9) : 0;
   // (the bias gradient comes out of the weight-gradient launch when both are asked for)
   const size_t cs_bytes = grad_b && !grad_w ? ufpn::colsum_workspace_bytes(pixels, 256) : 0;
   StreamScratch scratch(s);
-  cudaError_t e = scratch.alloc(wf_bytes + zb_bytes + dw_bytes + cs_bytes);
+  cudaError_t e = scratch.alloc(wf_bytes + dw_bytes + cs_bytes + 16);
   if (e != cudaSuccess) return cuda_fail(e, "backward scratch");
   uint8_t* base = static_cast<uint8_t*>(scratch.p);
   if (grad_x) {
-    float* zero_bias = reinterpret_cast<float*>(base + wf_bytes);
-    if ((e = cudaMemsetAsync(zero_bias, 0, zb_bytes, s)) != cudaSuccess) return cuda_fail(e, "memset");
-    if ((e = ufpn::launch_flip_conv3x3_weights(dt, w, base, s)) != cudaSuccess)
-      return cuda_fail(e, "flip weights");
+    const float* zero_bias = device_zeros();
+    if (!zero_bias) return fail(UFPN_ERR_CUDA, "device zeros");
+    const void* wf = w_f;
+    if (!wf) {
+      if ((e = ufpn::launch_flip_conv3x3_weights(dt, w, base, s)) != cudaSuccess)
+        return cuda_fail(e, "flip weights");
+      wf = base;
+    }
     ufpn::TcPlan plan;
-    e = ufpn::plan_tc_conv3x3(plan, dt, grad_out, base, zero_bias, grad_x, nullptr, N, H, W,
+    e = ufpn::plan_tc_conv3x3(plan, dt, grad_out, wf, zero_bias, grad_x, nullptr, N, H, W,
                               ufpn::halo_tiling(), device_status_word(), 0);
     if (e == cudaSuccess) e = ufpn::launch_tc(plan, s);
     if (e != cudaSuccess) return cuda_fail(e, "3x3 input gradient");
   }
   if (grad_w) {
-    float* ws = reinterpret_cast<float*>(base + wf_bytes + zb_bytes);
+    float* ws = reinterpret_cast<float*>(base + wf_bytes);
     e = ufpn::launch_dw_gemm(dt, grad_out, x, N, H, W, 256, 9, grad_w, grad_b, ws, dw_bytes,
                              device_status_word(), s);
     if (e != cudaSuccess) return cuda_fail(e, "3x3 weight gradient");
   }
   if (grad_b && !grad_w) {
-    float* ws = reinterpret_cast<float*>(base + wf_bytes + zb_bytes + dw_bytes);
+    float* ws = reinterpret_cast<float*>(base + wf_bytes + dw_bytes);
     e = ufpn::launch_colsum(dt, grad_out, pixels, 256, grad_b, ws, cs_bytes, s);
     if (e != cudaSuccess) return cuda_fail(e, "bias gradient");
   }
   return UFPN_OK;
+}
+
+int ufpn_lateral_conv_backward(int dtype, const void* x, const void* w, const void* grad_out,
+                               void* grad_x, float* grad_w, float* grad_b, int N, int Cin, int H,
+                               int W, void* stream) {
+  return lateral_backward(dtype, x, w, nullptr, grad_out, grad_x, grad_w, grad_b, N, Cin, H, W,
+                          stream);
+}
+
+int ufpn_lateral_conv_backward_t(int dtype, const void* x, const void* w_t, const void* grad_out,
+                                 void* grad_x, float* grad_w, float* grad_b, int N, int Cin,
+                                 int H, int W, void* stream) {
+  if (grad_x && !w_t) return fail(UFPN_ERR_INVALID_ARG, "NULL tensor pointer");
+  return lateral_backward(dtype, x, nullptr, w_t, grad_out, grad_x, grad_w, grad_b, N, Cin, H, W,
+                          stream);
+}
+
+int ufpn_conv3x3_backward(int dtype, const void* x, const void* w, const void* grad_out,
+                          void* grad_x, float* grad_w, float* grad_b, int N, int H, int W,
+                          void* stream) {
+  return conv3x3_backward(dtype, x, w, nullptr, grad_out, grad_x, grad_w, grad_b, N, H, W, stream);
+}
+
+int ufpn_conv3x3_backward_f(int dtype, const void* x, const void* w_flipped, const void* grad_out,
+                            void* grad_x, float* grad_w, float* grad_b, int N, int H, int W,
+                            void* stream) {
+  if (grad_x && !w_flipped) return fail(UFPN_ERR_INVALID_ARG, "NULL tensor pointer");
+  return conv3x3_backward(dtype, x, nullptr, w_flipped, grad_out, grad_x, grad_w, grad_b, N, H, W,
+                          stream);
+}
+
+int ufpn_prepare_neck_weights(int dtype, int levels, const float* const* lat_w, const int* cin,
+                              const float* const* conv_w, void* const* lat_out,
+                              void* const* lat_t_out, void* const* conv_packed,
+                              void* const* conv_flipped, void* stream) {
+  DType dt;
+  if (!parse_16bit(dtype, &dt)) return fail(UFPN_ERR_UNSUPPORTED, "weights go to bf16 or fp16");
+  if (levels < 1 || levels > 4 || !lat_w || !cin || !conv_w)
+    return fail(UFPN_ERR_INVALID_ARG, "levels must be 1..4 with input arrays");
+  ufpn::WeightPrepJob jobs[4 * 4];
+  int nj = 0;
+  for (int l = 0; l < levels; ++l) {
+    if (cin[l] <= 0 || cin[l] % 8 != 0) return fail(UFPN_ERR_UNSUPPORTED, "Cin must be a multiple of 8");
+    void* outs[4] = {lat_out ? lat_out[l] : nullptr, lat_t_out ? lat_t_out[l] : nullptr,
+                     conv_packed ? conv_packed[l] : nullptr, conv_flipped ? conv_flipped[l] : nullptr};
+    for (int k = 0; k < 4; ++k) {
+      if (!outs[k]) continue;
+      const float* in = k < 2 ? lat_w[l] : conv_w[l];
+      if (!in) return fail(UFPN_ERR_INVALID_ARG, "NULL weight pointer");
+      jobs[nj].kind = k;
+      jobs[nj].cin = cin[l];
+      jobs[nj].in = in;
+      jobs[nj].out = outs[k];
+      ++nj;
+    }
+  }
+  if (nj == 0) return UFPN_OK;
+  cudaError_t e = ufpn::launch_prepare_weights(dt, jobs, nj, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "prepare weights");
 }
 
 int ufpn_upsample_add_backward(int dtype, const void* grad_out, const void* base,

@@ -9,7 +9,7 @@ that library cannot be loaded the import fails: there is no CPU fallback.
 """
 from ._lib import UFPNError, lib  # noqa: F401  (raises ImportError without the library)
 from .core import UnifiedFPN, fpn_forward_pytorch
-from .ops import (device_status, fold_batch_norm, fpn_conv3x3, fpn_conv3x3_backward, fpn_conv3x3_fp8, fpn_conv3x3_fp8_from_bf16,
+from .ops import (device_status, fold_batch_norm, fpn_conv3x3, prepare_neck_weights, fpn_conv3x3_backward, fpn_conv3x3_fp8, fpn_conv3x3_fp8_from_bf16,
                   fpn_lateral_conv, fpn_lateral_conv_backward, fpn_lateral_conv_fp8, fpn_merge_two_levels, fpn_p6,
                   fpn_p6_backward, fpn_upsample_add, fpn_upsample_add_backward, fpn_upsample_bilinear,
                   pack_conv3x3_weight, quantize_fp8, quantize_fp8_rows)
@@ -21,7 +21,7 @@ __version__ = "1.0.0"
 
 __all__ = [
     "UnifiedFPN", "fpn_lateral_conv", "fpn_upsample_bilinear", "fpn_forward_pytorch",
-    "fpn_upsample_add", "fpn_merge_two_levels", "fpn_p6", "fpn_conv3x3", "fold_batch_norm", "pack_conv3x3_weight", "device_status",
+    "fpn_upsample_add", "fpn_merge_two_levels", "fpn_p6", "fpn_conv3x3", "fold_batch_norm", "prepare_neck_weights", "pack_conv3x3_weight", "device_status",
     "quantize_fp8", "quantize_fp8_rows", "fpn_lateral_conv_fp8", "fpn_conv3x3_fp8", "fpn_conv3x3_fp8_from_bf16", "HostPipeline",
     "benchmark_fpn", "profile_fpn", "get_device_info", "check_installation", "UFPNError",
     "fpn_lateral_conv_backward", "fpn_conv3x3_backward", "fpn_upsample_add_backward", "fpn_p6_backward",

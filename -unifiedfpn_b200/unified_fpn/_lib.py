@@ -92,6 +92,15 @@ SIGNATURES = {
     "ufpn_conv3x3_backward": (
         c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
                 c_void_p]),
+    "ufpn_lateral_conv_backward_t": (
+        c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                c_int, c_void_p]),
+    "ufpn_conv3x3_backward_f": (
+        c_int, [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
+                c_void_p]),
+    "ufpn_prepare_neck_weights": (
+        c_int, [c_int, c_int, POINTER(c_void_p), POINTER(c_int), POINTER(c_void_p), POINTER(c_void_p),
+                POINTER(c_void_p), POINTER(c_void_p), POINTER(c_void_p), c_void_p]),
     "ufpn_upsample_add_backward": (
         c_int, [c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p]),
     "ufpn_p6_backward": (c_int, [c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p]),

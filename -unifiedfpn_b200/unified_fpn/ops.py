@@ -229,23 +229,33 @@ def _cl16(t: torch.Tensor, what: str) -> torch.Tensor:
 
 
 def fpn_lateral_conv_backward(input: torch.Tensor, weight: torch.Tensor, grad_output: torch.Tensor,
-                              need_input_grad: bool = True):
+                              need_input_grad: bool = True, weight_t: torch.Tensor | None = None):
     """Gradients of ``fpn_lateral_conv(input, weight, bias)`` (16-bit, channels_last,
     Cout = 256): ``(grad_input, grad_weight [256, Cin] fp32, grad_bias [256] fp32)``;
     grad_input is None without ``need_input_grad``.  Reference: backward_lateral_conv_kernel
     (src/training/backward/lateral_conv_backward.cu:7-143), here deterministic: the weight
     gradient is a tensor-core GEMM over pixels, the input gradient the forward kernel with
-    the transposed weights."""
-    _check_cuda(input, weight, grad_output)
+    the transposed weights.  ``weight_t``: the weights already in that transposed layout
+    ([ceil(Cin/256)*256, 256] in the input's dtype, ``prepare_neck_weights``); ``weight`` is
+    then not read."""
+    _check_cuda(input, weight, grad_output, weight_t)
     x = _cl16(input, "input")
     g = _cl16(grad_output, "grad_output")
     N, Cin, H, W = x.shape
     if g.dtype != x.dtype or tuple(g.shape) != (N, 256, H, W):
         raise ValueError("grad_output must be [N, 256, H, W] in the input's dtype")
-    w = weight.reshape(256, Cin).to(device=x.device, dtype=x.dtype).contiguous()
     gx = torch.empty_like(x, memory_format=torch.channels_last) if need_input_grad else None
     gw = torch.empty(256, Cin, device=x.device, dtype=torch.float32)
     gb = torch.empty(256, device=x.device, dtype=torch.float32)
+    if weight_t is not None:
+        if weight_t.dtype != x.dtype or tuple(weight_t.shape) != ((Cin + 255) // 256 * 256, 256):
+            raise ValueError("weight_t must be [ceil(Cin/256)*256, 256] in the input's dtype")
+        check(lib.ufpn_lateral_conv_backward_t(dtype_code(x), x.data_ptr(), weight_t.contiguous().data_ptr(),
+                                               g.data_ptr(), gx.data_ptr() if gx is not None else None,
+                                               gw.data_ptr(), gb.data_ptr(), N, Cin, H, W, _stream(x)),
+              "ufpn_lateral_conv_backward_t")
+        return gx, gw, gb
+    w = weight.reshape(256, Cin).to(device=x.device, dtype=x.dtype).contiguous()
     check(lib.ufpn_lateral_conv_backward(dtype_code(x), x.data_ptr(), w.data_ptr(), g.data_ptr(),
                                          gx.data_ptr() if gx is not None else None, gw.data_ptr(),
                                          gb.data_ptr(), N, Cin, H, W, _stream(x)),
@@ -254,28 +264,69 @@ def fpn_lateral_conv_backward(input: torch.Tensor, weight: torch.Tensor, grad_ou
 
 
 def fpn_conv3x3_backward(input: torch.Tensor, weight: torch.Tensor, grad_output: torch.Tensor,
-                         need_input_grad: bool = True):
+                         need_input_grad: bool = True, weight_flipped: torch.Tensor | None = None):
     """Gradients of the 256 -> 256 pad-1 3x3 conv (``fpn_conv3x3``; 16-bit, channels_last):
     ``(grad_input, grad_weight [256, 256, 3, 3] fp32, grad_bias [256] fp32)``.  ``weight`` is
     [256, 256, 3, 3] (any float dtype) or packed [256, 9, 256] by ``pack_conv3x3_weight``.  The input
     gradient is the forward 3x3 kernel with the weights transposed in channels and flipped in
-    space; the weight gradient is a tensor-core GEMM over pixels (nine shifted taps)."""
-    _check_cuda(input, weight, grad_output)
+    space; the weight gradient is a tensor-core GEMM over pixels (nine shifted taps).
+    ``weight_flipped``: the weights already in that flipped layout ([256 c, 9, 256 o] in the
+    input's dtype, ``prepare_neck_weights``); ``weight`` is then not read."""
+    _check_cuda(input, weight, grad_output, weight_flipped)
     x = _cl16(input, "input")
     g = _cl16(grad_output, "grad_output")
     N, C, H, W = x.shape
     if C != 256 or g.dtype != x.dtype or tuple(g.shape) != (N, 256, H, W):
         raise ValueError("input and grad_output must be [N, 256, H, W] of one dtype")
+    gx = torch.empty_like(x, memory_format=torch.channels_last) if need_input_grad else None
+    gw = torch.empty(256, 256, 3, 3, device=x.device, dtype=torch.float32)
+    gb = torch.empty(256, device=x.device, dtype=torch.float32)
+    if weight_flipped is not None:
+        if weight_flipped.dtype != x.dtype or tuple(weight_flipped.shape) != (256, 9, 256):
+            raise ValueError("weight_flipped must be [256, 9, 256] in the input's dtype")
+        check(lib.ufpn_conv3x3_backward_f(dtype_code(x), x.data_ptr(), weight_flipped.contiguous().data_ptr(),
+                                          g.data_ptr(), gx.data_ptr() if gx is not None else None,
+                                          gw.data_ptr(), gb.data_ptr(), N, H, W, _stream(x)),
+              "ufpn_conv3x3_backward_f")
+        return gx, gw, gb
     wp = weight if (weight.dim() == 3 and weight.dtype == x.dtype) else pack_conv3x3_weight(weight, x.dtype)
     wp = wp.contiguous()
-    gx = torch.empty_like(x, memory_format=torch.channels_last) if need_input_grad else None
-    gw = torch.empty(256, 9, 256, device=x.device, dtype=torch.float32)
-    gb = torch.empty(256, device=x.device, dtype=torch.float32)
     check(lib.ufpn_conv3x3_backward(dtype_code(x), x.data_ptr(), wp.data_ptr(), g.data_ptr(),
                                     gx.data_ptr() if gx is not None else None, gw.data_ptr(),
                                     gb.data_ptr(), N, H, W, _stream(x)), "ufpn_conv3x3_backward")
-    # [o][tap][c] -> [o][c][ky][kx]
-    return gx, gw.permute(0, 2, 1).reshape(256, 256, 3, 3).contiguous(), gb
+    return gx, gw, gb
+
+
+def prepare_neck_weights(lateral_w, output_w, dtype: torch.dtype, backward: bool = True):
+    """Every per-step layout of the training path's weights from the fp32 masters in ONE
+    launch: ``(lateral [256, Cin], lateral_t [ceil(Cin/256)*256, 256], packed 3x3 [256, 9,
+    256], flipped 3x3 [256, 9, 256])`` as lists over the levels, in ``dtype`` (the last two
+    lists are None without ``backward``).  ``lateral_w``: [256, Cin] (or [256, Cin, 1, 1]),
+    ``output_w``: [256, 256, 3, 3]; fp32 CUDA tensors."""
+    if dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError("weights are prepared in bf16 or fp16")
+    n = len(lateral_w)
+    if n != len(output_w) or not 1 <= n <= 4:
+        raise ValueError("one lateral and one 3x3 weight per level (1..4 levels)")
+    lat = [w.detach().reshape(256, -1).to(torch.float32).contiguous() for w in lateral_w]
+    conv = [w.detach().to(torch.float32).contiguous() for w in output_w]
+    _check_cuda(*lat, *conv)
+    dev = lat[0].device
+    cin = [w.shape[1] for w in lat]
+    if any(tuple(w.shape) != (256, 256, 3, 3) for w in conv):
+        raise ValueError("3x3 weights must be [256, 256, 3, 3]")
+    lat16 = [torch.empty(256, c, device=dev, dtype=dtype) for c in cin]
+    packed = [torch.empty(256, 9, 256, device=dev, dtype=dtype) for _ in conv]
+    lat_t = [torch.empty((c + 255) // 256 * 256, 256, device=dev, dtype=dtype) for c in cin] if backward else None
+    flipped = [torch.empty(256, 9, 256, device=dev, dtype=dtype) for _ in conv] if backward else None
+    P = _lib.c_void_p * n
+
+    def ptrs(ts):
+        return P(*[t.data_ptr() for t in ts]) if ts is not None else None
+    check(lib.ufpn_prepare_neck_weights(_DT[dtype], n, ptrs(lat), (_lib.c_int * n)(*cin), ptrs(conv),
+                                        ptrs(lat16), ptrs(lat_t), ptrs(packed), ptrs(flipped),
+                                        _stream(lat[0])), "ufpn_prepare_neck_weights")
+    return lat16, lat_t, packed, flipped
 
 
 def fpn_upsample_add_backward(grad_output: torch.Tensor, coarse_size: tuple[int, int],

@@ -21,7 +21,7 @@ from typing import Sequence
 import torch
 
 from .ops import (fpn_conv3x3, fpn_conv3x3_backward, fpn_lateral_conv, fpn_lateral_conv_backward,
-                  fpn_p6_backward, fpn_upsample_add_backward, pack_conv3x3_weight)
+                  fpn_p6_backward, fpn_upsample_add_backward, prepare_neck_weights)
 
 _CL = torch.channels_last
 
@@ -39,16 +39,17 @@ def fpn_neck_forward_train(feats: Sequence[torch.Tensor], lateral_w: Sequence[to
     if dt not in (torch.bfloat16, torch.float16) or any(f.dtype != dt for f in feats):
         raise ValueError("training runs on bf16 or fp16 features of one dtype")
     x = [f.contiguous(memory_format=_CL) for f in feats]
-    lw = [w.reshape(256, -1).to(dtype=dt).contiguous() for w in lateral_w]
+    # every weight layout of the step (forward and backward) in one launch
+    lw, lw_t, packed, flipped = prepare_neck_weights(lateral_w, output_w, dt)
     merged = [None] * 4
     merged[3] = fpn_lateral_conv(x[3], lw[3], lateral_b[3])
     for l in (2, 1, 0):  # top-down: M_l = lateral(C_l) + up(M_{l+1}), fused in the lateral
         merged[l] = fpn_lateral_conv(x[l], lw[l], lateral_b[l], coarse=merged[l + 1])
-    packed = [pack_conv3x3_weight(w, dt) for w in output_w]
     outs = [fpn_conv3x3(merged[l], packed[l], output_b[l]) for l in range(3)]
     p5 = fpn_conv3x3(merged[3], packed[3], output_b[3], p6=return_p6)
     outs += list(p5) if return_p6 else [p5]
-    return outs, {"x": x, "merged": merged, "lateral_w": lw, "packed": packed}
+    return outs, {"x": x, "merged": merged, "lateral_w": lw, "lateral_w_t": lw_t, "packed": packed,
+                  "flipped": flipped}
 
 
 def fpn_neck_backward(grad_outputs: Sequence[torch.Tensor | None], saved: dict,
@@ -58,6 +59,7 @@ def fpn_neck_backward(grad_outputs: Sequence[torch.Tensor | None], saved: dict,
     ``grad_lateral_w`` ([256, Cin] fp32), ``grad_lateral_b``, ``grad_output_w``
     ([256, 256, 3, 3] fp32), ``grad_output_b``."""
     x, merged, lw, packed = saved["x"], saved["merged"], saved["lateral_w"], saved["packed"]
+    lw_t, flipped = saved.get("lateral_w_t"), saved.get("flipped")
     dt = x[0].dtype
 
     def g16(g, like):
@@ -70,12 +72,14 @@ def fpn_neck_backward(grad_outputs: Sequence[torch.Tensor | None], saved: dict,
         dp[3] = fpn_p6_backward(grad_outputs[4], dp[3].clone(memory_format=_CL))
     dm, gw3, gb3 = [None] * 4, [None] * 4, [None] * 4
     for l in range(4):
-        dm[l], gw3[l], gb3[l] = fpn_conv3x3_backward(merged[l], packed[l], dp[l])
+        dm[l], gw3[l], gb3[l] = fpn_conv3x3_backward(merged[l], packed[l], dp[l],
+                                                     weight_flipped=flipped[l] if flipped else None)
     for l in (1, 2, 3):  # adjoint of the top-down chain, finest first
         dm[l] = fpn_upsample_add_backward(dm[l - 1], tuple(merged[l].shape[2:]), base=dm[l])
     gx, gwl, gbl = [None] * 4, [None] * 4, [None] * 4
     for l in range(4):
-        gx[l], gwl[l], gbl[l] = fpn_lateral_conv_backward(x[l], lw[l], dm[l], need_input_grad)
+        gx[l], gwl[l], gbl[l] = fpn_lateral_conv_backward(x[l], lw[l], dm[l], need_input_grad,
+                                                          weight_t=lw_t[l] if lw_t else None)
     return {"grad_inputs": gx if need_input_grad else None, "grad_lateral_w": gwl,
             "grad_lateral_b": gbl, "grad_output_w": gw3, "grad_output_b": gb3}
 

@@ -42,12 +42,12 @@ METRIC_FP8 = "FPN-neck images/sec, FP8 (e4m3) R50 640×640, 16 images/GPU @1/2/4
 METRIC_TRAIN = "FPN-neck training steps (forward + backward, all gradients) images/sec, R50 800×1216"
 R50_CHANNELS = (256, 512, 1024, 2048)
 # Library kernels per training step (FPNNeck forward + backward with gradients for P2..P6):
-# forward per level: 3x3 weight packing, lateral (with the fused top-down add), 3x3 (+P6);
-# backward per level: 3x3 weight flip, input gradient, weight-gradient GEMM (bias gradient
-# included) + its reduction; lateral: weight transpose, input gradient (one launch for all
-# channel slices), weight-gradient GEMM + reduction; the P6 adjoint once and the top-down
-# adjoint for P3, P4, P5.
-TRAIN_LAUNCHES = 4 * 3 + 4 * 4 + 4 * 4 + 1 + 3
+# one launch preparing every weight layout of the step; forward per level: lateral (with the
+# fused top-down add), 3x3 (+P6); backward per level: 3x3 input gradient, weight-gradient GEMM
+# (bias gradient included) + its reduction; lateral input gradient (one launch for all channel
+# slices), weight-gradient GEMM + reduction; the P6 adjoint once and the top-down adjoint for
+# P3, P4, P5.
+TRAIN_LAUNCHES = 1 + 4 * 2 + 4 * 3 + 4 * 3 + 1 + 3
 
 
 def level_sizes(h, w):

@@ -266,16 +266,29 @@ cudaError_t launch_tc(const TcPlan& plan, cudaStream_t s, LaunchOpts opts = Laun
 
 // ---- backward pass (backward.cu).  Reference: src/training/backward/lateral_conv_backward.cu
 // :7-143 and upsample_backward.cu:4-80; here the exact adjoints of the forward, deterministic.
-// Weight gradient dW[o][t][c] = sum_p dY[p][o] X[p + shift(t)][c] (fp32, [256][taps][Cin];
+// Weight gradient dW[o][c][t] = sum_p dY[p][o] X[p + shift(t)][c] (fp32, [256][Cin][taps];
 // taps 1 = the 1x1 lateral, 9 = the pad-1 3x3 with shift(t) = (t / 3 - 1, t % 3 - 1)) of
 // NHWC dY [N][H][W][256] and X [N][H][W][Cin] (16-bit): a tensor-core GEMM over pixels with
 // fp32 split-K partials in `workspace` (dw_gemm_workspace_bytes) added in a fixed order.
 size_t dw_gemm_workspace_bytes(int N, int H, int W, int Cin, int taps);
-// With grad_b (nullable), grad_b[o] = sum_p dY[p][o] comes out of the same launch: one unit's
-// CTAs also sum the dY tiles they stream (fixed-order partials, reduced with dW).
+// With grad_b (nullable), grad_b[o] = sum_p dY[p][o] comes out of the same launch: the idle
+// epilogue warps of the channel-block-0 CTAs sum dY (fixed-order partials, reduced with dW).
 cudaError_t launch_dw_gemm(DType dt, const void* grad_out, const void* x, int N, int H, int W,
                            int Cin, int taps, float* grad_w, float* grad_b, float* workspace,
                            size_t ws_bytes, int* status, cudaStream_t s);
+// Per-step weight layouts of the training path from fp32 master weights, all in one launch.
+// kind 0: lateral [256][cin] -> 16-bit [256][cin]; 1: the same transposed, [cblk * 256][256]
+// (cblk = ceil(cin / 256), zero rows from cin); 2: 3x3 [256 o][256 c][3][3] -> packed
+// [256 o][9 t][256 c]; 3: the same flipped for the input gradient, [256 c][9 t][256 o] holding
+// w[o][c][8 - t].  Rounding as launch_pack_conv3x3 (to nearest even).
+struct WeightPrepJob {
+  int kind = 0;
+  int cin = 0;
+  const float* in = nullptr;
+  void* out = nullptr;
+};
+cudaError_t launch_prepare_weights(DType dt, const WeightPrepJob* jobs, int num_jobs,
+                                   cudaStream_t s);
 // out[c] = sum over the pixels of g[p][c] (fp32; per block, then in a fixed order).
 size_t colsum_workspace_bytes(long long pixels, int C);
 cudaError_t launch_colsum(DType dt, const void* g, long long pixels, int C, float* out,

@@ -193,16 +193,37 @@ int ufpn_merge_two_levels(int dtype, const void* m5, const void* l4, void* m4, v
  * dtype BF16/F16, NHWC maps; weight and bias gradients are fp32; any output pointer may be
  * NULL to skip that gradient.  Scratch is allocated stream-ordered on `stream`. */
 /* grad_x [N][H][W][Cin] = grad_out . w; grad_w [256][Cin] = sum_p grad_out^T x;
- * grad_b [256] = sum_p grad_out.  w is the packed lateral weight [256][Cin] in dtype. */
+ * grad_b [256] = sum_p grad_out.  w is the packed lateral weight [256][Cin] in dtype;
+ * Cin a multiple of 8, at most 2048. */
 int ufpn_lateral_conv_backward(int dtype, const void* x, const void* w, const void* grad_out,
                                void* grad_x, float* grad_w, float* grad_b, int N, int Cin, int H,
                                int W, void* stream);
+/* The same with w already transposed for the input gradient: w_t [ceil(Cin/256)*256][256]
+ * (ufpn_prepare_neck_weights kind "lateral transposed"). */
+int ufpn_lateral_conv_backward_t(int dtype, const void* x, const void* w_t, const void* grad_out,
+                                 void* grad_x, float* grad_w, float* grad_b, int N, int Cin,
+                                 int H, int W, void* stream);
 /* 3x3 pad-1 conv 256 -> 256: grad_x = conv3x3(grad_out, w flipped and transposed);
- * grad_w [256][9][256] (packed order: output channel, tap, input channel); grad_b [256].
+ * grad_w [256][256][3][3] (output channel, input channel, ky, kx); grad_b [256].
  * w is the packed weight [256][9][256] (ufpn_pack_conv3x3_weights). */
 int ufpn_conv3x3_backward(int dtype, const void* x, const void* w, const void* grad_out,
                           void* grad_x, float* grad_w, float* grad_b, int N, int H, int W,
                           void* stream);
+/* The same with the weights already flipped for the input gradient: w_flipped
+ * [256 c][9 t][256 o] = w[o][c][8 - t] (ufpn_prepare_neck_weights). */
+int ufpn_conv3x3_backward_f(int dtype, const void* x, const void* w_flipped, const void* grad_out,
+                            void* grad_x, float* grad_w, float* grad_b, int N, int H, int W,
+                            void* stream);
+/* Every per-step weight layout of the training path from the fp32 master weights in ONE
+ * launch, for `levels` levels (1..4): lat_out[l] = lateral [256][cin[l]] in dtype, lat_t_out[l]
+ * = its transpose [ceil(cin/256)*256][256] (zero rows from cin), conv_packed[l] = the 3x3
+ * [256][9][256] as ufpn_pack_conv3x3_weights, conv_flipped[l] = [256 c][9][256 o] =
+ * w[o][c][8 - t].  lat_w[l]: fp32 [256][cin[l]], conv_w[l]: fp32 [256][256][3][3]; any output
+ * array, or entry, may be NULL to skip it. */
+int ufpn_prepare_neck_weights(int dtype, int levels, const float* const* lat_w, const int* cin,
+                              const float* const* conv_w, void* const* lat_out,
+                              void* const* lat_t_out, void* const* conv_packed,
+                              void* const* conv_flipped, void* stream);
 /* Top-down add: grad_coarse = base (or 0) + bilinear^T(grad_out) [N][Hc][Wc][C] (the lateral's
  * gradient is grad_out itself). */
 int ufpn_upsample_add_backward(int dtype, const void* grad_out, const void* base,

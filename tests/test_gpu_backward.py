@@ -214,3 +214,33 @@ def test_graphed_training_step_matches_eager(cuda_device):
             for p in neck.parameters():
                 p.mul_(0.5)
     assert U.device_status() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_prepared_weights_and_their_backward_paths(cuda_device, dtype):
+    """prepare_neck_weights (one launch, every layout) equals the separate conversions
+    bitwise, and the backward entry points that take the prepared transposed / flipped weights
+    give bitwise the gradients of the ones that derive them."""
+    import unified_fpn as U
+    g = torch.Generator().manual_seed(61)
+    cins = (128, 512, 1024, 2048)
+    lat = [(torch.randn(256, c, generator=g) * 0.05).to(cuda_device) for c in cins]
+    conv = [(torch.randn(256, 256, 3, 3, generator=g) * 0.03).to(cuda_device) for _ in cins]
+    lw, lw_t, packed, flipped = U.prepare_neck_weights(lat, conv, dtype)
+    for l, c in enumerate(cins):
+        assert torch.equal(lw[l], lat[l].to(dtype))
+        ref_t = torch.zeros((c + 255) // 256 * 256, 256, dtype=dtype, device=cuda_device)
+        ref_t[:c] = lat[l].to(dtype).t()
+        assert torch.equal(lw_t[l], ref_t)
+        assert torch.equal(packed[l], U.pack_conv3x3_weight(conv[l], dtype))
+        assert torch.equal(flipped[l], packed[l].flip(1).permute(2, 1, 0))
+    x = _cl(torch.randn(1, 512, 19, 27, generator=g).to(dtype).to(cuda_device))
+    gy = _cl(torch.randn(1, 256, 19, 27, generator=g).to(dtype).to(cuda_device))
+    a = U.fpn_lateral_conv_backward(x, lw[1], gy)
+    b = U.fpn_lateral_conv_backward(x, lw[1], gy, weight_t=lw_t[1])
+    assert all(torch.equal(p, q) for p, q in zip(a, b))
+    m = _cl(torch.randn(1, 256, 19, 27, generator=g).to(dtype).to(cuda_device))
+    a = U.fpn_conv3x3_backward(m, packed[0], gy)
+    b = U.fpn_conv3x3_backward(m, packed[0], gy, weight_flipped=flipped[0])
+    assert all(torch.equal(p, q) for p, q in zip(a, b))
+    assert U.device_status() == 0
