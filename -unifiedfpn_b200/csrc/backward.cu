@@ -349,6 +349,51 @@ __global__ void __launch_bounds__(256) reduce_partials_kernel(const float* __res
   }
 }
 
+// Sum over s of v(s) in the fixed order of reduce_partials_kernel: four running sums over
+// s = 0, 4, .. / 1, 5, .. / .., then (a0 + a1) + (a2 + a3).
+template <typename F>
+__device__ __forceinline__ float fixed_order_sum(int n, F v) {
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+  int s = 0;
+  for (; s + 4 <= n; s += 4) {
+    a0 += v(s);
+    a1 += v(s + 1);
+    a2 += v(s + 2);
+    a3 += v(s + 3);
+  }
+  if (s < n) a0 += v(s);
+  if (s + 1 < n) a1 += v(s + 1);
+  if (s + 2 < n) a2 += v(s + 2);
+  return (a0 + a1) + (a2 + a3);
+}
+
+// 3x3 weight gradient in [256 o][Cin c][9 t] order: block (o, c0) sums partial[s][t][o][c0 + cc]
+// for its 9 x 32 outputs (thread (t, cc): coalesced 128-byte reads per t), stages them as
+// [cc][t] and writes the 288 contiguous outputs in order.  The last block (with grad_b) sums
+// the bias partials.  Same fixed order as reduce_partials_kernel.
+__global__ void __launch_bounds__(288) reduce_partials_taps9_kernel(
+    const float* __restrict__ partial, float* __restrict__ out, int ksplit, int Cin,
+    const float* __restrict__ db_partial, float* __restrict__ grad_b, int db_rows) {
+  __shared__ float tile[32 * 9];
+  const int cblocks = (Cin + 31) / 32;
+  if (static_cast<int>(blockIdx.x) == 256 * cblocks) {  // bias
+    const int o = threadIdx.x;
+    if (o < 256)
+      grad_b[o] = fixed_order_sum(db_rows, [&](int r) { return __ldg(db_partial + r * 256 + o); });
+    return;
+  }
+  const int o = static_cast<int>(blockIdx.x) / cblocks;
+  const int c0 = (static_cast<int>(blockIdx.x) % cblocks) * 32;
+  const int t = threadIdx.x / 32, cc = threadIdx.x % 32;
+  const long long per = 9LL * 256 * Cin;
+  const size_t idx = (static_cast<size_t>(t) * 256 + o) * Cin + c0 + cc;
+  if (c0 + cc < Cin)
+    tile[cc * 9 + t] = fixed_order_sum(ksplit, [&](int s) { return __ldg(partial + s * per + idx); });
+  __syncthreads();
+  const int j = threadIdx.x;  // output element c0 * 9 + j of row o
+  if (c0 + j / 9 < Cin) out[(static_cast<size_t>(o) * Cin + c0) * 9 + j] = tile[j];
+}
+
 // ------------------------------------------------------------------ bias gradient
 template <typename T>
 __device__ __forceinline__ float bw_to_f(T v) {
@@ -786,7 +831,7 @@ __global__ void __launch_bounds__(256) p6_adjoint_kernel(const T* __restrict__ g
 // ------------------------------------------------------------------ weight layouts
 constexpr int kPrepMaxJobs = 16;
 struct PrepArgs {
-  long long begin[kPrepMaxJobs + 1];  // flat element range of job j: [begin[j], begin[j + 1])
+  int first_block[kPrepMaxJobs + 1];  // blocks of job j: [first_block[j], first_block[j + 1])
   const float* in[kPrepMaxJobs];
   void* out[kPrepMaxJobs];
   int kind[kPrepMaxJobs];
@@ -794,43 +839,54 @@ struct PrepArgs {
   int num_jobs;
 };
 
-// Every output element of every job (WeightPrepJob kinds), one launch, writes coalesced.
+// One block per unit of a job (WeightPrepJob kinds), 256 threads; every thread reads adjacent
+// fp32 words and every warp writes consecutive elements.
+//   kind 0: unit = output row o;      out[o][c] = in[o][c]
+//   kind 1: unit = 8 rows c0 .. c0+7; out[c][o] = in[o][c] (0 for c >= cin), thread o
+//   kind 2: unit = output channel o;  out[o][t][c] = in[o][c][t], thread c
+//   kind 3: unit = input channel c;   out[c][t][o] = in[o][c][8 - t], thread o
 template <typename T>
 __global__ void __launch_bounds__(256) prepare_weights_kernel(const __grid_constant__ PrepArgs a) {
-  const long long total = a.begin[a.num_jobs];
-  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    int j = 0;
-    while (j + 1 < a.num_jobs && i >= a.begin[j + 1]) ++j;
-    const long long k = i - a.begin[j];
-    const float* in = a.in[j];
-    const int cin = a.cin[j];
-    float v;
-    switch (a.kind[j]) {
-      case 0:  // [o][c]
-        v = in[k];
-        break;
-      case 1: {  // [c][o] <- [o][c], zero rows c >= cin
-        const int c = static_cast<int>(k >> 8), o = static_cast<int>(k & 255);
-        v = c < cin ? in[static_cast<size_t>(o) * cin + c] : 0.f;
-        break;
-      }
-      case 2: {  // [o][t][c] <- [o][c][t]
-        const int c = static_cast<int>(k & 255);
-        const int t = static_cast<int>((k >> 8) % 9);
-        const int o = static_cast<int>(k / 2304);
-        v = in[(static_cast<size_t>(o) * 256 + c) * 9 + t];
-        break;
-      }
-      default: {  // [c][t][o] <- [o][c][8 - t]
-        const int o = static_cast<int>(k & 255);
-        const int t = static_cast<int>((k >> 8) % 9);
-        const int c = static_cast<int>(k / 2304);
-        v = in[(static_cast<size_t>(o) * 256 + c) * 9 + (8 - t)];
-        break;
-      }
+  int j = 0;
+  while (j + 1 < a.num_jobs && static_cast<int>(blockIdx.x) >= a.first_block[j + 1]) ++j;
+  const int u = static_cast<int>(blockIdx.x) - a.first_block[j];
+  const float* in = a.in[j];
+  T* out = static_cast<T*>(a.out[j]);
+  const int cin = a.cin[j];
+  const int t0 = threadIdx.x;
+  switch (a.kind[j]) {
+    case 0:
+      for (int c = t0; c < cin; c += 256)
+        out[static_cast<size_t>(u) * cin + c] = bw_from_f<T>(in[static_cast<size_t>(u) * cin + c]);
+      break;
+    case 1: {
+      const int c0 = u * 8;
+      float v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        v[i] = c0 + i < cin ? in[static_cast<size_t>(t0) * cin + c0 + i] : 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) out[static_cast<size_t>(c0 + i) * 256 + t0] = bw_from_f<T>(v[i]);
+      break;
     }
-    static_cast<T*>(a.out[j])[k] = bw_from_f<T>(v);
+    case 2: {
+      const float* src = in + (static_cast<size_t>(u) * 256 + t0) * 9;
+      float v[9];
+#pragma unroll
+      for (int t = 0; t < 9; ++t) v[t] = src[t];
+#pragma unroll
+      for (int t = 0; t < 9; ++t) out[(static_cast<size_t>(u) * 9 + t) * 256 + t0] = bw_from_f<T>(v[t]);
+      break;
+    }
+    default: {
+      const float* src = in + (static_cast<size_t>(t0) * 256 + u) * 9;
+      float v[9];
+#pragma unroll
+      for (int t = 0; t < 9; ++t) v[t] = src[8 - t];
+#pragma unroll
+      for (int t = 0; t < 9; ++t) out[(static_cast<size_t>(u) * 9 + t) * 256 + t0] = bw_from_f<T>(v[t]);
+      break;
+    }
   }
 }
 // out[c][r] = in[r][c] for an R x C matrix (rows of out beyond C up to out_rows are zeroed)
@@ -952,6 +1008,13 @@ cudaError_t launch_dw_gemm(DType dt, const void* grad_out, const void* x, int N,
   e = launch_ex(kern, dim3(grid), dim3(kTcThreads), kDwSmemBytes, s, LaunchOpts(), 1, map_g, map_x,
                 map_p, a);
   if (e != cudaSuccess) return e;
+  if (taps == 9) {
+    // one block per (output channel, 32 input channels) + one for the bias
+    const unsigned grid9 = static_cast<unsigned>(256 * ((Cin + 31) / 32) + (grad_b ? 1 : 0));
+    return launch_ex(reduce_partials_taps9_kernel, dim3(grid9), dim3(288), 0, s, LaunchOpts(), 1,
+                     static_cast<const float*>(workspace), grad_w, a.ksplit, Cin,
+                     static_cast<const float*>(a.db_partial), grad_b, a.ksplit * taps);
+  }
   const long long per = static_cast<long long>(taps) * 256 * Cin + (grad_b ? 256 : 0);
   return launch_ex(reduce_partials_kernel, dim3(grid_for(per, 256)), dim3(256), 0, s, LaunchOpts(),
                    1, static_cast<const float*>(workspace), grad_w, a.ksplit, taps, Cin,
@@ -1023,21 +1086,20 @@ cudaError_t launch_prepare_weights(DType dt, const WeightPrepJob* jobs, int num_
   if (num_jobs < 1 || num_jobs > kPrepMaxJobs || !jobs) return cudaErrorInvalidValue;
   PrepArgs a;
   std::memset(&a, 0, sizeof(a));
-  long long at = 0;
+  int blocks = 0;
   for (int j = 0; j < num_jobs; ++j) {
     const WeightPrepJob& jb = jobs[j];
     if (!jb.in || !jb.out || jb.kind < 0 || jb.kind > 3 || jb.cin <= 0) return cudaErrorInvalidValue;
-    a.begin[j] = at;
+    a.first_block[j] = blocks;
     a.in[j] = jb.in;
     a.out[j] = jb.out;
     a.kind[j] = jb.kind;
     a.cin[j] = jb.cin;
-    const long long cblk = (jb.cin + 255) / 256;
-    at += jb.kind == 0 ? 256LL * jb.cin : jb.kind == 1 ? cblk * 256 * 256 : 256LL * 9 * 256;
+    blocks += jb.kind == 1 ? (jb.cin + 255) / 256 * 32 : 256;  // kind 1: 8-row units
   }
-  a.begin[num_jobs] = at;
+  a.first_block[num_jobs] = blocks;
   a.num_jobs = num_jobs;
-  const unsigned grid = grid_for(at, 256);
+  const unsigned grid = static_cast<unsigned>(blocks);
   switch (dt) {
     case DType::BF16:
       return launch_ex(prepare_weights_kernel<__nv_bfloat16>, dim3(grid), dim3(256), 0, s,
