@@ -993,17 +993,14 @@ cudaError_t launch_dw_gemm(DType dt, const void* grad_out, const void* x, int N,
   if ((e = encode_rows_map(&map_p, DType::F32, workspace, Cin,
                            static_cast<long long>(a.ksplit) * taps * 256, 32, 32)) != cudaSuccess)
     return e;
-  static bool configured[2][64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
+  static std::atomic<bool> configured[2][64];  // per dtype and device
   const int ti = dt == DType::BF16 ? 0 : 1;
   auto kern = dt == DType::BF16 ? fpn_dw_gemm_kernel<__nv_bfloat16> : fpn_dw_gemm_kernel<__half>;
-  if (dev < 64 && !configured[ti][dev]) {
-    if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  kDwSmemBytes)) != cudaSuccess)
-      return e;
-    configured[ti][dev] = true;
-  }
+  if ((e = once_per_device(configured[ti], [&] {
+         return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kDwSmemBytes);
+       })) != cudaSuccess)
+    return e;
   const int grid = units * a.ksplit;
   e = launch_ex(kern, dim3(grid), dim3(kTcThreads), kDwSmemBytes, s, LaunchOpts(), 1, map_g, map_x,
                 map_p, a);
@@ -1068,15 +1065,11 @@ cudaError_t launch_colsum(DType dt, const void* g, long long pixels, int C, floa
 template <typename K, typename... Args>
 cudaError_t launch_staged_adjoint(K kernel, long long blocks, size_t smem, cudaStream_t s,
                                   Args... args) {
-  static std::atomic<bool> opted[64];  // per device: the attribute belongs to its context
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
+  static std::atomic<bool> opted[64];
+  cudaError_t e = once_per_device(opted, [&] {
+    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+  });
   if (e != cudaSuccess) return e;
-  if (dev >= 64 || !opted[dev].load(std::memory_order_acquire)) {
-    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-    if (e != cudaSuccess) return e;
-    if (dev < 64) opted[dev].store(true, std::memory_order_release);
-  }
   return launch_ex(kernel, dim3(static_cast<unsigned>(blocks)), dim3(kUaThreads), smem, s,
                    LaunchOpts(), 1, args...);
 }

@@ -494,17 +494,16 @@ struct StreamScratch {
   void* p = nullptr;
   explicit StreamScratch(cudaStream_t st) : s(st) {}
   cudaError_t alloc(size_t bytes) {
-    static bool cached[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 64 && !cached[dev]) {
+    static std::atomic<bool> cached[64];
+    ufpn::once_per_device(cached, [] {
+      int dev = 0;
       cudaMemPool_t pool;
-      if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
-        uint64_t keep = UINT64_MAX;
-        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
-      }
-      cached[dev] = true;
-    }
+      cudaError_t e = cudaGetDevice(&dev);
+      if (e == cudaSuccess) e = cudaDeviceGetDefaultMemPool(&pool, dev);
+      uint64_t keep = UINT64_MAX;
+      if (e == cudaSuccess) e = cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+      return e;
+    });
     return cudaMallocAsync(&p, bytes > 0 ? bytes : 16, s);
   }
   ~StreamScratch() {

@@ -911,18 +911,19 @@ cudaError_t upsample_add_t(const void* coarse, const void* lat, void* out, int N
         const long long units = static_cast<long long>(N) * H * chunks;
         auto kern = upsample_add_px512_kernel<T, kPx512Batch>;
         // grid = the blocks resident at once, each with a contiguous run of units
-        static int resident[64] = {};
+        static std::atomic<int> resident[64];
         int dev = 0;
         cudaGetDevice(&dev);
-        if (dev < 64 && resident[dev] == 0) {
+        const bool cached = dev >= 0 && dev < 64;
+        int res = cached ? resident[dev].load(std::memory_order_relaxed) : 0;
+        if (res == 0) {
           int per_sm = 0;
           cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, 0);
           if (e != cudaSuccess) return e;
-          int sms = 0;
-          cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-          resident[dev] = (per_sm > 0 ? per_sm : 1) * (sms > 0 ? sms : 148);
+          res = (per_sm > 0 ? per_sm : 1) * sm_count();
+          if (cached) resident[dev].store(res, std::memory_order_relaxed);
         }
-        const long long g = units < resident[dev < 64 ? dev : 0] ? units : resident[dev < 64 ? dev : 0];
+        const long long g = units < res ? units : res;
         if (g <= 0) return cudaSuccess;
         const long long per = (units + g - 1) / g;
         if (per >= (1LL << 31)) return cudaErrorInvalidValue;

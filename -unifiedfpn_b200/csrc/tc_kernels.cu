@@ -140,16 +140,11 @@ void fill_tiling(TcGemmArgs& a, int N, int H, int W, Conv3x3Tiling t) {
 
 template <int kMode, typename T>
 cudaError_t launch_t(const TcPlan& p, cudaStream_t s, LaunchOpts opts) {
-  static bool configured[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(fpn_tc_gemm_kernel<kMode, T>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         TcCfgT<kMode, T>::kSmemBytes);
-    if (e != cudaSuccess) return e;
-    configured[dev] = true;
-  }
+  static std::atomic<bool> configured[64];
+  cudaError_t e = once_per_device(configured, [] {
+    return cudaFuncSetAttribute(fpn_tc_gemm_kernel<kMode, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfgT<kMode, T>::kSmemBytes);
+  });
+  if (e != cudaSuccess) return e;
   TcGemmArgs a;
   std::memcpy(&a, p.args, sizeof(a));
   return launch_ex(fpn_tc_gemm_kernel<kMode, T>, dim3(p.grid), dim3(TcCfgT<kMode, T>::kThreads),
@@ -159,16 +154,11 @@ cudaError_t launch_t(const TcPlan& p, cudaStream_t s, LaunchOpts opts) {
 
 template <typename T>
 cudaError_t launch_halo_t(const TcPlan& p, cudaStream_t s, LaunchOpts opts) {
-  static bool configured[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(fpn_conv3x3_halo_kernel<T>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         HaloCfg::kSmemBytes);
-    if (e != cudaSuccess) return e;
-    configured[dev] = true;
-  }
+  static std::atomic<bool> configured[64];
+  cudaError_t e = once_per_device(configured, [] {
+    return cudaFuncSetAttribute(fpn_conv3x3_halo_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, HaloCfg::kSmemBytes);
+  });
+  if (e != cudaSuccess) return e;
   TcGemmArgs a;
   std::memcpy(&a, p.args, sizeof(a));
   return launch_ex(fpn_conv3x3_halo_kernel<T>, dim3(p.grid), dim3(kTcThreads),
@@ -177,16 +167,11 @@ cudaError_t launch_halo_t(const TcPlan& p, cudaStream_t s, LaunchOpts opts) {
 
 template <typename T, bool kCvt = false>
 cudaError_t launch_halo_pair_t(const TcPlan& p, cudaStream_t s, LaunchOpts opts) {
-  static bool configured[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(fpn_conv3x3_halo_pair_kernel<T, kCvt>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         PairCfgT<kCvt>::kSmemBytes);
-    if (e != cudaSuccess) return e;
-    configured[dev] = true;
-  }
+  static std::atomic<bool> configured[64];
+  cudaError_t e = once_per_device(configured, [] {
+    return cudaFuncSetAttribute(fpn_conv3x3_halo_pair_kernel<T, kCvt>, cudaFuncAttributeMaxDynamicSharedMemorySize, PairCfgT<kCvt>::kSmemBytes);
+  });
+  if (e != cudaSuccess) return e;
   TcGemmArgs a;
   std::memcpy(&a, p.args, sizeof(a));
   return launch_ex(fpn_conv3x3_halo_pair_kernel<T, kCvt>, dim3(p.grid),
@@ -196,16 +181,11 @@ cudaError_t launch_halo_pair_t(const TcPlan& p, cudaStream_t s, LaunchOpts opts)
 
 template <typename T>
 cudaError_t launch_lateral_pair_t(const TcPlan& p, cudaStream_t s, LaunchOpts opts) {
-  static bool configured[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(fpn_lateral_pair_kernel<T>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         LpCfg::kSmemBytes);
-    if (e != cudaSuccess) return e;
-    configured[dev] = true;
-  }
+  static std::atomic<bool> configured[64];
+  cudaError_t e = once_per_device(configured, [] {
+    return cudaFuncSetAttribute(fpn_lateral_pair_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, LpCfg::kSmemBytes);
+  });
+  if (e != cudaSuccess) return e;
   TcGemmArgs a;
   std::memcpy(&a, p.args, sizeof(a));
   return launch_ex(fpn_lateral_pair_kernel<T>, dim3(p.grid), dim3(kTcThreads), LpCfg::kSmemBytes,
@@ -215,16 +195,17 @@ cudaError_t launch_lateral_pair_t(const TcPlan& p, cudaStream_t s, LaunchOpts op
 }  // namespace
 
 int sm_count() {
-  static int counts[64] = {};
+  static std::atomic<int> counts[64];
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 64) dev = 63;
-  if (counts[dev] == 0) {
-    int n = 0;
+  const bool cached = dev >= 0 && dev < 64;
+  int n = cached ? counts[dev].load(std::memory_order_relaxed) : 0;
+  if (n == 0) {
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    counts[dev] = n > 0 ? n : 148;
+    if (n <= 0) n = 148;
+    if (cached) counts[dev].store(n, std::memory_order_relaxed);
   }
-  return counts[dev];
+  return n;
 }
 
 Conv3x3Tiling default_tiling(int H, int W) {
@@ -660,16 +641,11 @@ cudaError_t plan_neck(NeckPlan& plan, DType dt, int N, const NeckLevel* lv, void
 namespace {
 template <typename T>
 cudaError_t launch_neck_t(const NeckPlan& p, cudaStream_t s, LaunchOpts opts) {
-  static bool configured[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(fpn_neck_kernel<T>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kNeckSmemBytes);
-    if (e != cudaSuccess) return e;
-    configured[dev] = true;
-  }
+  static std::atomic<bool> configured[64];
+  cudaError_t e = once_per_device(configured, [] {
+    return cudaFuncSetAttribute(fpn_neck_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kNeckSmemBytes);
+  });
+  if (e != cudaSuccess) return e;
   const NeckParams* P = reinterpret_cast<const NeckParams*>(p.params);
   return launch_ex(fpn_neck_kernel<T>, dim3(p.grid), dim3(kTcThreads), kNeckSmemBytes, s, opts,
                    1, *P);

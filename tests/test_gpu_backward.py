@@ -244,3 +244,45 @@ def test_prepared_weights_and_their_backward_paths(cuda_device, dtype):
     b = U.fpn_conv3x3_backward(m, packed[0], gy, weight_flipped=flipped[0])
     assert all(torch.equal(p, q) for p, q in zip(a, b))
     assert U.device_status() == 0
+
+
+def test_training_step_full_size_properties(cuda_device):
+    """R50 800x1216 batch 2 (the benchmark's size, beyond the oracle's reach at fp32 autograd):
+    two eager steps give bitwise the same gradients, all finite; the graphed step gives them
+    too; the bias gradients equal the pixel sums of the output gradients they come from (dP5's
+    includes P6's through the P6 adjoint)."""
+    import unified_fpn as U
+    dev = torch.device(cuda_device)
+    sizes = O.level_sizes(800, 1216)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(71)
+    feats = [_cl(torch.randn(2, c, h, w, device=dev, generator=gen).clamp_min_(0).to(torch.bfloat16))
+             .requires_grad_() for c, (h, w) in zip(O.R50_CHANNELS, sizes)]
+    osz = list(sizes) + [((sizes[3][0] - 1) // 2 + 1, (sizes[3][1] - 1) // 2 + 1)]
+    grads = [_cl(torch.randn(2, 256, h, w, device=dev, generator=gen).to(torch.bfloat16)) for h, w in osz]
+    neck = U.FPNNeck(O.R50_CHANNELS).to(dev)
+
+    def step(fn):
+        for p in neck.parameters():
+            p.grad = None
+        for f in feats:
+            f.grad = None
+        torch.autograd.backward(fn(feats), grads)
+        torch.cuda.synchronize()
+        return [p.grad.clone() for p in neck.parameters()] + [f.grad.clone() for f in feats]
+
+    a = step(neck)
+    b = step(neck)
+    assert all(torch.equal(x, y) for x, y in zip(a, b))
+    assert all(torch.isfinite(x).all() for x in a)
+    # output-conv bias gradients: the sums of dP2..dP5 (dP5 with dP6 scattered in)
+    ob = list(neck.output_b)
+    for l in range(3):
+        ref = grads[l].float().sum(dim=(0, 2, 3))
+        assert O.rel_err(ob[l].grad.cpu(), ref.cpu()) < 1e-5
+    ref5 = grads[3].float().sum(dim=(0, 2, 3)) + grads[4].float().sum(dim=(0, 2, 3))
+    assert O.rel_err(ob[3].grad.cpu(), ref5.cpu()) < 1e-3  # (dP5 + dP6 rounded to bf16 once)
+    run = neck.make_graphed([f.detach().clone().requires_grad_() for f in feats])
+    c = step(run)
+    assert all(torch.equal(x, y) for x, y in zip(a, c))
+    assert U.device_status() == 0
