@@ -45,8 +45,9 @@ def fpn_neck_forward_train(feats: Sequence[torch.Tensor], lateral_w: Sequence[to
     merged[3] = fpn_lateral_conv(x[3], lw[3], lateral_b[3])
     for l in (2, 1, 0):  # top-down: M_l = lateral(C_l) + up(M_{l+1}), fused in the lateral
         merged[l] = fpn_lateral_conv(x[l], lw[l], lateral_b[l], coarse=merged[l + 1])
-    outs = [fpn_conv3x3(merged[l], packed[l], output_b[l]) for l in range(3)]
-    p5 = fpn_conv3x3(merged[3], packed[3], output_b[3], p6=return_p6)
+    # halo tiles on CTA pairs (tile_w=-1), as the inference engine runs its 3x3s
+    outs = [fpn_conv3x3(merged[l], packed[l], output_b[l], tile_w=-1) for l in range(3)]
+    p5 = fpn_conv3x3(merged[3], packed[3], output_b[3], p6=return_p6, tile_w=-1)
     outs += list(p5) if return_p6 else [p5]
     return outs, {"x": x, "merged": merged, "lateral_w": lw, "lateral_w_t": lw_t, "packed": packed,
                   "flipped": flipped}
