@@ -706,6 +706,105 @@ int ufpn_prepare_neck_weights(int dtype, int levels, const float* const* lat_w, 
   return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "prepare weights");
 }
 
+int ufpn_neck_train_forward(int dtype, int N, const int* cin, const int* H, const int* W,
+                            const void* const* x, const float* const* lat_w,
+                            const float* const* lat_b, const float* const* conv_w,
+                            const float* const* conv_b, void* const* lat16, void* const* lat16_t,
+                            void* const* packed, void* const* flipped, void* const* merged,
+                            void* const* out, void* p6, void* stream) {
+  DType dt;
+  if (!parse_16bit(dtype, &dt)) return fail(UFPN_ERR_UNSUPPORTED, "training runs on bf16 or fp16");
+  if (N <= 0 || !cin || !H || !W || !x || !lat_w || !lat_b || !conv_w || !conv_b || !lat16 ||
+      !packed || !merged || !out)
+    return fail(UFPN_ERR_INVALID_ARG, "NULL argument");
+  for (int l = 0; l < 4; ++l)
+    if (!x[l] || !lat_w[l] || !lat_b[l] || !conv_w[l] || !conv_b[l] || !lat16[l] || !packed[l] ||
+        !merged[l] || !out[l] || H[l] <= 0 || W[l] <= 0)
+      return fail(UFPN_ERR_INVALID_ARG, "level arguments must be non-NULL with positive sizes");
+  int rc = ufpn_prepare_neck_weights(dtype, 4, lat_w, cin, conv_w, lat16, lat16_t, packed,
+                                     flipped, stream);
+  if (rc != UFPN_OK) return rc;
+  for (int l = 3; l >= 0; --l) {  // top-down: M_l = lateral(C_l) + up(M_{l+1})
+    rc = ufpn_lateral_conv(dtype, UFPN_LAYOUT_NHWC, x[l], lat16[l], lat_b[l],
+                           l < 3 ? merged[l + 1] : nullptr, merged[l], N, cin[l], H[l], W[l], 256,
+                           l < 3 ? H[l + 1] : 0, l < 3 ? W[l + 1] : 0, stream);
+    if (rc != UFPN_OK) return rc;
+  }
+  for (int l = 0; l < 4; ++l) {  // 3x3s on CTA-pair halo tiles
+    rc = ufpn_conv3x3_act(dtype, merged[l], packed[l], conv_b[l], out[l], l == 3 ? p6 : nullptr, N,
+                          H[l], W[l], -1, 0, 0.01f, stream);
+    if (rc != UFPN_OK) return rc;
+  }
+  return UFPN_OK;
+}
+
+int ufpn_neck_train_backward(int dtype, int N, const int* cin, const int* H, const int* W,
+                             const void* const* x, const void* const* merged,
+                             const void* const* lat16_t, const void* const* flipped,
+                             const void* const* grad_out, const void* grad_p6,
+                             void* const* grad_x, float* const* grad_lat_w,
+                             float* const* grad_lat_b, float* const* grad_conv_w,
+                             float* const* grad_conv_b, void* stream) {
+  DType dt;
+  if (!parse_16bit(dtype, &dt)) return fail(UFPN_ERR_UNSUPPORTED, "training runs on bf16 or fp16");
+  if (N <= 0 || !cin || !H || !W || !x || !merged || !lat16_t || !flipped || !grad_out ||
+      !grad_lat_w || !grad_lat_b || !grad_conv_w || !grad_conv_b)
+    return fail(UFPN_ERR_INVALID_ARG, "NULL argument");
+  for (int l = 0; l < 4; ++l)
+    if (!x[l] || !merged[l] || !lat16_t[l] || !flipped[l] || !grad_lat_w[l] || !grad_lat_b[l] ||
+        !grad_conv_w[l] || !grad_conv_b[l] || H[l] <= 0 || W[l] <= 0)
+      return fail(UFPN_ERR_INVALID_ARG, "level arguments must be non-NULL with positive sizes");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t esz = ufpn::dtype_size(dt);
+  size_t map_bytes[4], off[6] = {0};
+  for (int l = 0; l < 4; ++l) {
+    map_bytes[l] = (static_cast<size_t>(N) * H[l] * W[l] * 256 * esz + 255) / 256 * 256;
+    off[l + 1] = off[l] + map_bytes[l];
+  }
+  // scratch: dM2..dM5, then dP5 + P6's scatter (if dP6) or a zero map for an absent dP_l
+  size_t zero_bytes = 0;
+  for (int l = 0; l < 4; ++l)
+    if (!grad_out[l] && map_bytes[l] > zero_bytes) zero_bytes = map_bytes[l];
+  const size_t dp5_bytes = grad_p6 ? map_bytes[3] : 0;
+  StreamScratch scratch(s);
+  cudaError_t e = scratch.alloc(off[4] + zero_bytes + dp5_bytes + 16);
+  if (e != cudaSuccess) return cuda_fail(e, "train backward scratch");
+  uint8_t* base = static_cast<uint8_t*>(scratch.p);
+  void* dm[4];
+  for (int l = 0; l < 4; ++l) dm[l] = base + off[l];
+  void* zeros = zero_bytes ? base + off[4] : nullptr;
+  if (zeros && (e = cudaMemsetAsync(zeros, 0, zero_bytes, s)) != cudaSuccess)
+    return cuda_fail(e, "memset");
+  const void* dp[4];
+  for (int l = 0; l < 4; ++l) dp[l] = grad_out[l] ? grad_out[l] : zeros;
+  int rc;
+  if (grad_p6) {  // dP5 += P6^T(dP6), into a copy (the caller's dP5 stays as given)
+    void* dp5 = base + off[4] + zero_bytes;
+    if ((e = cudaMemcpyAsync(dp5, dp[3], static_cast<size_t>(N) * H[3] * W[3] * 256 * esz,
+                             cudaMemcpyDeviceToDevice, s)) != cudaSuccess)
+      return cuda_fail(e, "copy dP5");
+    if ((rc = ufpn_p6_backward(dtype, grad_p6, dp5, N, 256, H[3], W[3], stream)) != UFPN_OK)
+      return rc;
+    dp[3] = dp5;
+  }
+  for (int l = 0; l < 4; ++l) {  // every level's 3x3 backward: dM_l, dW3_l, db3_l
+    rc = conv3x3_backward(dtype, merged[l], nullptr, flipped[l], dp[l], dm[l], grad_conv_w[l],
+                          grad_conv_b[l], N, H[l], W[l], stream);
+    if (rc != UFPN_OK) return rc;
+  }
+  for (int l = 1; l < 4; ++l) {  // top-down adjoint, finest first: dM_l += up^T(dM_{l-1})
+    rc = ufpn_upsample_add_backward(dtype, dm[l - 1], dm[l], dm[l], N, 256, H[l], W[l], H[l - 1],
+                                    W[l - 1], stream);
+    if (rc != UFPN_OK) return rc;
+  }
+  for (int l = 0; l < 4; ++l) {  // laterals: dC_l, dWlat_l, dblat_l
+    rc = lateral_backward(dtype, x[l], nullptr, lat16_t[l], dm[l], grad_x ? grad_x[l] : nullptr,
+                          grad_lat_w[l], grad_lat_b[l], N, cin[l], H[l], W[l], stream);
+    if (rc != UFPN_OK) return rc;
+  }
+  return UFPN_OK;
+}
+
 int ufpn_upsample_add_backward(int dtype, const void* grad_out, const void* base,
                                void* grad_coarse, int N, int C, int Hc, int Wc, int H, int W,
                                void* stream) {

@@ -11,8 +11,10 @@ backward needs; ``fpn_neck_backward`` returns the gradients of every input, weig
     dM_l += up^T(dM_{l-1}) for l = P3, P4, P5 (finest first: the top-down adjoint)
     dC_l, dWlat_l, dblat_l = lateral^T(C_l, Wlat_l, dM_l)
 
-``FPNNeck`` wraps both in a ``torch.nn.Module`` with fp32 master weights (the kernels compute in
-the features' 16-bit dtype) for use under autograd.
+Each half is one call into the library's native driver (``ufpn_neck_train_forward`` /
+``ufpn_neck_train_backward``), which issues its kernels on the caller's stream; Python only
+allocates the results.  ``FPNNeck`` wraps both in a ``torch.nn.Module`` with fp32 master weights
+(the kernels compute in the features' 16-bit dtype) for use under autograd.
 """
 from __future__ import annotations
 
@@ -20,10 +22,19 @@ from typing import Sequence
 
 import torch
 
-from .ops import (fpn_conv3x3, fpn_conv3x3_backward, fpn_lateral_conv, fpn_lateral_conv_backward,
-                  fpn_p6_backward, fpn_upsample_add_backward, prepare_neck_weights)
+from . import _lib
+from ._lib import check, lib
+from .ops import _DT
 
 _CL = torch.channels_last
+
+
+def _ptrs(ts):
+    return (_lib.c_void_p * len(ts))(*[t.data_ptr() if t is not None else None for t in ts])
+
+
+def _ints(vs):
+    return (_lib.c_int * len(vs))(*vs)
 
 
 def fpn_neck_forward_train(feats: Sequence[torch.Tensor], lateral_w: Sequence[torch.Tensor],
@@ -32,23 +43,43 @@ def fpn_neck_forward_train(feats: Sequence[torch.Tensor], lateral_w: Sequence[to
     """Forward of the neck for training.  ``feats``: C2..C5 (bf16 / fp16, 4-D CUDA); weights
     as for ``UnifiedFPN.initialize_weights`` (lateral [256, Cin], 3x3 [256, 256, 3, 3], fp32
     biases).  Returns ``(outputs, saved)``: P2..P5 (and P6) channels_last, and the state
-    ``fpn_neck_backward`` needs (the inputs, the merged maps M2..M5, the packed weights)."""
-    if len(feats) != 4:
-        raise ValueError("feats must be C2..C5")
+    ``fpn_neck_backward`` needs (the inputs, the merged maps M2..M5, the prepared weights).
+    One library call (``ufpn_neck_train_forward``): the weight layouts of the whole step in
+    one launch, the four laterals top-down, the four 3x3s (CTA-pair halo tiles)."""
+    if len(feats) != 4 or len(lateral_w) != 4 or len(output_w) != 4:
+        raise ValueError("feats and weights must be C2..C5 / four levels")
     dt = feats[0].dtype
     if dt not in (torch.bfloat16, torch.float16) or any(f.dtype != dt for f in feats):
         raise ValueError("training runs on bf16 or fp16 features of one dtype")
+    if any(not f.is_cuda for f in feats) or feats[0].dim() != 4:
+        raise ValueError("features must be 4-D CUDA tensors")
+    dev = feats[0].device
     x = [f.contiguous(memory_format=_CL) for f in feats]
-    # every weight layout of the step (forward and backward) in one launch
-    lw, lw_t, packed, flipped = prepare_neck_weights(lateral_w, output_w, dt)
-    merged = [None] * 4
-    merged[3] = fpn_lateral_conv(x[3], lw[3], lateral_b[3])
-    for l in (2, 1, 0):  # top-down: M_l = lateral(C_l) + up(M_{l+1}), fused in the lateral
-        merged[l] = fpn_lateral_conv(x[l], lw[l], lateral_b[l], coarse=merged[l + 1])
-    # halo tiles on CTA pairs (tile_w=-1), as the inference engine runs its 3x3s
-    outs = [fpn_conv3x3(merged[l], packed[l], output_b[l], tile_w=-1) for l in range(3)]
-    p5 = fpn_conv3x3(merged[3], packed[3], output_b[3], p6=return_p6, tile_w=-1)
-    outs += list(p5) if return_p6 else [p5]
+    N = x[0].shape[0]
+    cin = [f.shape[1] for f in x]
+    H = [f.shape[2] for f in x]
+    W = [f.shape[3] for f in x]
+    lat32 = [w.detach().reshape(256, -1).to(device=dev, dtype=torch.float32).contiguous() for w in lateral_w]
+    conv32 = [w.detach().to(device=dev, dtype=torch.float32).contiguous() for w in output_w]
+    latb = [b.detach().to(device=dev, dtype=torch.float32).contiguous() for b in lateral_b]
+    convb = [b.detach().to(device=dev, dtype=torch.float32).contiguous() for b in output_b]
+    if any(w.shape[1] != c for w, c in zip(lat32, cin)) or any(tuple(w.shape) != (256, 256, 3, 3) for w in conv32):
+        raise ValueError("lateral weights must be [256, Cin] and 3x3 weights [256, 256, 3, 3]")
+    lw = [torch.empty(256, c, device=dev, dtype=dt) for c in cin]
+    lw_t = [torch.empty((c + 255) // 256 * 256, 256, device=dev, dtype=dt) for c in cin]
+    packed = [torch.empty(256, 9, 256, device=dev, dtype=dt) for _ in cin]
+    flipped = [torch.empty(256, 9, 256, device=dev, dtype=dt) for _ in cin]
+    merged = [torch.empty(N, 256, h, w, device=dev, dtype=dt, memory_format=_CL) for h, w in zip(H, W)]
+    outs = [torch.empty(N, 256, h, w, device=dev, dtype=dt, memory_format=_CL) for h, w in zip(H, W)]
+    p6 = torch.empty(N, 256, (H[3] - 1) // 2 + 1, (W[3] - 1) // 2 + 1, device=dev, dtype=dt,
+                     memory_format=_CL) if return_p6 else None
+    check(lib.ufpn_neck_train_forward(_DT[dt], N, _ints(cin), _ints(H), _ints(W), _ptrs(x), _ptrs(lat32),
+                                      _ptrs(latb), _ptrs(conv32), _ptrs(convb), _ptrs(lw), _ptrs(lw_t),
+                                      _ptrs(packed), _ptrs(flipped), _ptrs(merged), _ptrs(outs),
+                                      p6.data_ptr() if p6 is not None else None,
+                                      torch.cuda.current_stream(dev).cuda_stream), "ufpn_neck_train_forward")
+    if return_p6:
+        outs.append(p6)
     return outs, {"x": x, "merged": merged, "lateral_w": lw, "lateral_w_t": lw_t, "packed": packed,
                   "flipped": flipped}
 
@@ -58,31 +89,40 @@ def fpn_neck_backward(grad_outputs: Sequence[torch.Tensor | None], saved: dict,
     """Gradients of the neck given dP2..dP5 (and dP6; None = zero) and ``saved`` from
     ``fpn_neck_forward_train``.  Returns a dict: ``grad_inputs`` (dC2..dC5, or None),
     ``grad_lateral_w`` ([256, Cin] fp32), ``grad_lateral_b``, ``grad_output_w``
-    ([256, 256, 3, 3] fp32), ``grad_output_b``."""
-    x, merged, lw, packed = saved["x"], saved["merged"], saved["lateral_w"], saved["packed"]
-    lw_t, flipped = saved.get("lateral_w_t"), saved.get("flipped")
+    ([256, 256, 3, 3] fp32), ``grad_output_b``.  One library call
+    (``ufpn_neck_train_backward``)."""
+    x, merged, lw_t, flipped = saved["x"], saved["merged"], saved["lateral_w_t"], saved["flipped"]
     dt = x[0].dtype
+    dev = x[0].device
+    N = x[0].shape[0]
+    cin = [f.shape[1] for f in x]
+    H = [f.shape[2] for f in x]
+    W = [f.shape[3] for f in x]
 
-    def g16(g, like):
+    def g16(g, shape):
         if g is None:
-            return torch.zeros_like(like, memory_format=_CL)
-        return g.to(dtype=dt).contiguous(memory_format=_CL)
+            return None
+        if tuple(g.shape) != shape:
+            raise ValueError(f"output gradient of shape {tuple(g.shape)}, expected {shape}")
+        return g.to(device=dev, dtype=dt).contiguous(memory_format=_CL)
 
-    dp = [g16(grad_outputs[l] if l < len(grad_outputs) else None, merged[l]) for l in range(4)]
+    dp = [g16(grad_outputs[l] if l < len(grad_outputs) else None, (N, 256, H[l], W[l])) for l in range(4)]
+    g6 = None
     if len(grad_outputs) > 4 and grad_outputs[4] is not None:
-        dp[3] = fpn_p6_backward(grad_outputs[4], dp[3].clone(memory_format=_CL))
-    dm, gw3, gb3 = [None] * 4, [None] * 4, [None] * 4
-    for l in range(4):
-        dm[l], gw3[l], gb3[l] = fpn_conv3x3_backward(merged[l], packed[l], dp[l],
-                                                     weight_flipped=flipped[l] if flipped else None)
-    for l in (1, 2, 3):  # adjoint of the top-down chain, finest first
-        dm[l] = fpn_upsample_add_backward(dm[l - 1], tuple(merged[l].shape[2:]), base=dm[l])
-    gx, gwl, gbl = [None] * 4, [None] * 4, [None] * 4
-    for l in range(4):
-        gx[l], gwl[l], gbl[l] = fpn_lateral_conv_backward(x[l], lw[l], dm[l], need_input_grad,
-                                                          weight_t=lw_t[l] if lw_t else None)
-    return {"grad_inputs": gx if need_input_grad else None, "grad_lateral_w": gwl,
-            "grad_lateral_b": gbl, "grad_output_w": gw3, "grad_output_b": gb3}
+        g6 = g16(grad_outputs[4], (N, 256, (H[3] - 1) // 2 + 1, (W[3] - 1) // 2 + 1))
+    gx = [torch.empty_like(f, memory_format=_CL) for f in x] if need_input_grad else None
+    gwl = [torch.empty(256, c, device=dev, dtype=torch.float32) for c in cin]
+    gbl = [torch.empty(256, device=dev, dtype=torch.float32) for _ in cin]
+    gw3 = [torch.empty(256, 256, 3, 3, device=dev, dtype=torch.float32) for _ in cin]
+    gb3 = [torch.empty(256, device=dev, dtype=torch.float32) for _ in cin]
+    check(lib.ufpn_neck_train_backward(_DT[dt], N, _ints(cin), _ints(H), _ints(W), _ptrs(x), _ptrs(merged),
+                                       _ptrs(lw_t), _ptrs(flipped), _ptrs(dp),
+                                       g6.data_ptr() if g6 is not None else None,
+                                       _ptrs(gx) if gx is not None else None, _ptrs(gwl), _ptrs(gbl),
+                                       _ptrs(gw3), _ptrs(gb3), torch.cuda.current_stream(dev).cuda_stream),
+          "ufpn_neck_train_backward")
+    return {"grad_inputs": gx, "grad_lateral_w": gwl, "grad_lateral_b": gbl, "grad_output_w": gw3,
+            "grad_output_b": gb3}
 
 
 class _NeckFunction(torch.autograd.Function):

@@ -224,6 +224,30 @@ int ufpn_prepare_neck_weights(int dtype, int levels, const float* const* lat_w, 
                               const float* const* conv_w, void* const* lat_out,
                               void* const* lat_t_out, void* const* conv_packed,
                               void* const* conv_flipped, void* stream);
+/* Training step of the whole neck in two calls (C2..C5 = level 0..3, NHWC 16-bit, batch N,
+ * level sizes H[l] x W[l], input channels cin[l]; fp32 master weights as for
+ * ufpn_prepare_neck_weights, fp32 biases [256]).
+ * Forward: prepares the weight layouts (lat16, lat16_t, packed, flipped: caller-allocated as
+ * in ufpn_prepare_neck_weights; lat16_t / flipped may be NULL for inference), computes the
+ * merged maps M2..M5 (merged[l], [N][H][W][256]) top-down and P2..P5 (out[l]) with P6 (p6, or
+ * NULL) -- the forward of UnifiedFPN on the training kernels.
+ * Backward: from dP2..dP5 (grad_out[l], 16-bit NHWC; NULL = zero) and dP6 (grad_p6 or NULL) and
+ * the forward's x, merged, lat16_t and flipped, writes dC_l (grad_x[l]; grad_x or an entry
+ * NULL skips it) and the fp32 gradients of every weight ([256][cin] lateral, [256][256][3][3]
+ * 3x3) and bias; the scratch for dM2..dM5 is stream-ordered on `stream`. */
+int ufpn_neck_train_forward(int dtype, int N, const int* cin, const int* H, const int* W,
+                            const void* const* x, const float* const* lat_w,
+                            const float* const* lat_b, const float* const* conv_w,
+                            const float* const* conv_b, void* const* lat16, void* const* lat16_t,
+                            void* const* packed, void* const* flipped, void* const* merged,
+                            void* const* out, void* p6, void* stream);
+int ufpn_neck_train_backward(int dtype, int N, const int* cin, const int* H, const int* W,
+                             const void* const* x, const void* const* merged,
+                             const void* const* lat16_t, const void* const* flipped,
+                             const void* const* grad_out, const void* grad_p6,
+                             void* const* grad_x, float* const* grad_lat_w,
+                             float* const* grad_lat_b, float* const* grad_conv_w,
+                             float* const* grad_conv_b, void* stream);
 /* Top-down add: grad_coarse = base (or 0) + bilinear^T(grad_out) [N][Hc][Wc][C] (the lateral's
  * gradient is grad_out itself). */
 int ufpn_upsample_add_backward(int dtype, const void* grad_out, const void* base,
