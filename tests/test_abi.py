@@ -75,6 +75,15 @@ def test_host_side_argument_validation():
     assert lib.ufpn_conv3x3_backward(2, 16, 16, 18, 16, None, None, 1, 4, 4, None) == _lib.ERR_ALIGNMENT
     assert lib.ufpn_upsample_add_backward(2, 16, None, 16, 1, 256, 8, 8, 4, 4, None) == _lib.ERR_UNSUPPORTED
     assert lib.ufpn_p6_backward(2, 16, 16, 1, 256, -3, 4, None) == _lib.ERR_INVALID_ARG
+    # training drivers: 16-bit only, every level argument required
+    assert lib.ufpn_neck_train_forward(0, 1, None, None, None, None, None, None, None, None, None, None,
+                                       None, None, None, None, None, None) == _lib.ERR_UNSUPPORTED
+    assert lib.ufpn_neck_train_forward(2, 1, None, None, None, None, None, None, None, None, None, None,
+                                       None, None, None, None, None, None) == _lib.ERR_INVALID_ARG
+    assert lib.ufpn_neck_train_backward(2, 0, None, None, None, None, None, None, None, None, None,
+                                        None, None, None, None, None, None) == _lib.ERR_INVALID_ARG
+    assert lib.ufpn_prepare_neck_weights(2, 5, None, None, None, None, None, None, None, None) == \
+        _lib.ERR_INVALID_ARG
     # activation codes are 0..3
     assert lib.ufpn_conv3x3_act(2, 16, 16, 16, 16, None, 1, 8, 8, 0, 7, 0.01, None) == _lib.ERR_INVALID_ARG
     assert lib.ufpn_core_set_activation(None, 1, 0.01) == _lib.ERR_INVALID_ARG

@@ -56,3 +56,20 @@ def test_fold_batch_norm_rejects_bad_parameters():
         U.fold_batch_norm(w, None, None, None, torch.zeros(4), -torch.ones(4))  # var + eps <= 0
     with pytest.raises(ValueError):
         U.fold_batch_norm(w, None, None, None, torch.zeros(3), torch.ones(3))
+
+
+def test_training_entry_points_validate_on_the_host():
+    """The training path rejects what it cannot run before any device work."""
+    import unified_fpn as U
+    feats = [torch.zeros(1, c, 4, 4, dtype=torch.bfloat16) for c in (256, 512, 1024, 2048)]
+    w = [torch.zeros(256, c) for c in (256, 512, 1024, 2048)]
+    b = [torch.zeros(256) for _ in range(4)]
+    w3 = [torch.zeros(256, 256, 3, 3) for _ in range(4)]
+    with pytest.raises(ValueError):  # CPU tensors
+        U.fpn_neck_forward_train(feats, w, b, w3, b)
+    with pytest.raises(ValueError):  # fp32 features
+        U.fpn_neck_forward_train([f.float() for f in feats], w, b, w3, b)
+    with pytest.raises(ValueError):  # three levels
+        U.fpn_neck_forward_train(feats[:3], w, b, w3, b)
+    with pytest.raises(ValueError):
+        U.prepare_neck_weights(w, w3, torch.float32)
