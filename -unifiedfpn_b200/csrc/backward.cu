@@ -297,6 +297,38 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 }
 
+// Sum over s < n of v(s) in a fixed order: four running sums over s = 0, 4, 8, .. / 1, 5, .. /
+// .., then (a0 + a1) + (a2 + a3).  Sixteen loads are issued before their adds (the sums keep
+// that association), so a thread has 16 loads in flight instead of 4.
+template <typename F>
+__device__ __forceinline__ float fixed_order_sum(int n, F v) {
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+  int s = 0;
+  for (; s + 16 <= n; s += 16) {
+    float t[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) t[i] = v(s + i);
+#pragma unroll
+    for (int i = 0; i < 16; i += 4) {
+      a0 += t[i];
+      a1 += t[i + 1];
+      a2 += t[i + 2];
+      a3 += t[i + 3];
+    }
+  }
+  for (; s + 4 <= n; s += 4) {
+    const float t0 = v(s), t1 = v(s + 1), t2 = v(s + 2), t3 = v(s + 3);
+    a0 += t0;
+    a1 += t1;
+    a2 += t2;
+    a3 += t3;
+  }
+  if (s < n) a0 += v(s);
+  if (s + 1 < n) a1 += v(s + 1);
+  if (s + 2 < n) a2 += v(s + 2);
+  return (a0 + a1) + (a2 + a3);
+}
+
 // out[(o * Cin + c) * taps + t] = sum over s of partial[s][t][o][c] (for the 3x3 the
 // [256][256][3][3] order of its fp32 weights), in a fixed order: four
 // running sums over s = 0, 4, 8, .. / 1, 5, 9, .. / .., added last (four loads in flight per
@@ -315,56 +347,16 @@ __global__ void __launch_bounds__(256) reduce_partials_kernel(const float* __res
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     if (i >= per) {
       const int o = static_cast<int>(i - per);
-      float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
-      int s = 0;
-      for (; s + 4 <= db_rows; s += 4) {
-        b0 += __ldg(db_partial + s * 256 + o);
-        b1 += __ldg(db_partial + (s + 1) * 256 + o);
-        b2 += __ldg(db_partial + (s + 2) * 256 + o);
-        b3 += __ldg(db_partial + (s + 3) * 256 + o);
-      }
-      if (s < db_rows) b0 += __ldg(db_partial + s * 256 + o);
-      if (s + 1 < db_rows) b1 += __ldg(db_partial + (s + 1) * 256 + o);
-      if (s + 2 < db_rows) b2 += __ldg(db_partial + (s + 2) * 256 + o);
-      grad_b[o] = (b0 + b1) + (b2 + b3);
+      grad_b[o] = fixed_order_sum(db_rows, [&](int r) { return __ldg(db_partial + r * 256 + o); });
       continue;
     }
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-    int s = 0;
-    for (; s + 4 <= ksplit; s += 4) {
-      a0 += __ldg(partial + s * per + i);
-      a1 += __ldg(partial + (s + 1) * per + i);
-      a2 += __ldg(partial + (s + 2) * per + i);
-      a3 += __ldg(partial + (s + 3) * per + i);
-    }
-    if (s < ksplit) a0 += __ldg(partial + s * per + i);
-    if (s + 1 < ksplit) a1 += __ldg(partial + (s + 1) * per + i);
-    if (s + 2 < ksplit) a2 += __ldg(partial + (s + 2) * per + i);
-    const float acc = (a0 + a1) + (a2 + a3);
+    const float acc = fixed_order_sum(ksplit, [&](int sp) { return __ldg(partial + sp * per + i); });
     const int c = static_cast<int>(i % Cin);
     const long long to = i / Cin;
     const int o = static_cast<int>(to % 256);
     const int t = static_cast<int>(to / 256);
     out[(static_cast<size_t>(o) * Cin + c) * taps + t] = acc;  // [o][c][ky][kx] (taps 9)
   }
-}
-
-// Sum over s of v(s) in the fixed order of reduce_partials_kernel: four running sums over
-// s = 0, 4, .. / 1, 5, .. / .., then (a0 + a1) + (a2 + a3).
-template <typename F>
-__device__ __forceinline__ float fixed_order_sum(int n, F v) {
-  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-  int s = 0;
-  for (; s + 4 <= n; s += 4) {
-    a0 += v(s);
-    a1 += v(s + 1);
-    a2 += v(s + 2);
-    a3 += v(s + 3);
-  }
-  if (s < n) a0 += v(s);
-  if (s + 1 < n) a1 += v(s + 1);
-  if (s + 2 < n) a2 += v(s + 2);
-  return (a0 + a1) + (a2 + a3);
 }
 
 // 3x3 weight gradient in [256 o][Cin c][9 t] order: block (o, c0) sums partial[s][t][o][c0 + cc]

@@ -290,3 +290,33 @@ def test_neck_activation(cuda_device, act, alpha, mode):
     ref0 = O.fpn_neck(feats, wts) if dtype == torch.float32 else O.fpn_neck(
         [O.round_to(f, dtype) for f in feats], rw)
     _check(plain, ref0, TOL32 if dtype == torch.float32 else TOL16)
+
+
+@pytest.mark.parametrize("case", [
+    ("config 3 shard: R50 1024x1024, 8 images", O.R50_CHANNELS, (1024, 1024), 8, "normal"),
+    ("config 4a: 128..1024 channels, 1344x1344, 8 images", O.SWIN_CHANNELS, (1344, 1344), 8, "normal"),
+])
+def test_neck_large_configs_against_oracle(cuda_device, case):
+    """The per-GPU shards of the larger configurations: the whole batch through the engine,
+    the first and last images against the oracle (fp32 on the same bf16-rounded inputs and
+    weights), and each of those images alone gives bitwise its slice of the batch result."""
+    import unified_fpn as U
+    _, chans, (h, w), batch, dist = case
+    sizes = O.level_sizes(h, w)
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(h + batch)
+    xin = [_cl(torch.randn(batch, c, hh, ww, device=dev, generator=gen).to(torch.bfloat16))
+           for c, (hh, ww) in zip(chans, sizes)]
+    wts = O.make_weights(chans, seed=h, bias_scale=0.1)
+    fpn = U.UnifiedFPN()
+    fpn.initialize_weights(wts.lat_w, wts.lat_b, wts.out_w, wts.out_b)
+    outs = [o.clone() for o in _run(fpn, xin)]
+    assert fpn.device_status() == 0
+    rw = O.NeckWeights([O.round_to(w_, torch.bfloat16) for w_ in wts.lat_w], wts.lat_b,
+                       [O.round_to(w_, torch.bfloat16) for w_ in wts.out_w], wts.out_b)
+    for n in (0, batch - 1):
+        ref = O.fpn_neck([x[n:n + 1].float().cpu() for x in xin], rw)
+        _check([o[n:n + 1] for o in outs], ref, TOL16)
+        alone = _run(fpn, [x[n:n + 1].contiguous(memory_format=torch.channels_last) for x in xin])
+        assert all(torch.equal(a, o[n:n + 1]) for a, o in zip(alone, outs))
