@@ -73,3 +73,18 @@ def test_training_entry_points_validate_on_the_host():
         U.fpn_neck_forward_train(feats[:3], w, b, w3, b)
     with pytest.raises(ValueError):
         U.prepare_neck_weights(w, w3, torch.float32)
+
+
+def test_batch_norm_identity_known_answer_of_the_reference_unit_test():
+    """tests/unit/test_fpn_kernels.cu:185-240 (BatchNorm): weight 1, bias 0, mean 0, var 1,
+    eps 1e-5 preserve the input within 1e-4 -- for the oracle's batch_norm and for a conv
+    folded with those parameters."""
+    import unified_fpn as U
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(2, 64, 8, 8, generator=g)
+    ones, zeros = torch.ones(64), torch.zeros(64)
+    assert (O.batch_norm(x, ones, zeros, zeros, ones, 1e-5) - x).abs().max() <= 1e-4
+    w = torch.randn(64, 64, generator=g) * 0.1
+    b = torch.randn(64, generator=g)
+    wf, bf = U.fold_batch_norm(w, b, ones, zeros, zeros, ones, eps=1e-5)
+    assert (wf - w).abs().max() <= 1e-4 * w.abs().max() and (bf - b).abs().max() <= 1e-4

@@ -199,3 +199,21 @@ def test_fp8_neck_accuracy_vs_fp32():
 
 def test_level_sizes_r50_800x1216():
     assert O.level_sizes(800, 1216) == [(200, 304), (100, 152), (50, 76), (25, 38)]
+
+
+def test_oracle_bilinear_ramp_closed_form():
+    """The ramp of the reference's BilinearUpsampleAccuracy unit test
+    (tests/unit/test_fpn_kernels.cu:113-180): x + 16 y on 16 x 16, upsampled to 32 x 32 with
+    scale in/out and half-pixel centres.  Output (16, 16) samples source (7.75, 7.75), so its
+    value is 7.75 + 16 * 7.75 = 131.75 in every channel.  (That unit test expects in_h * in_w / 4
+    = 64 +- 2 at the centre, which no bilinear of this ramp gives -- the ramp's own centre value
+    is 127.5 -- so it is no usable pin; the oracle is pinned to the reference's compiled host
+    function through tests/golden/bilinear_ref.npz instead.)"""
+    ramp = np.array([[x + 16 * y for x in range(16)] for y in range(16)], dtype=np.float32)
+    x = np.broadcast_to(ramp, (1, 64, 16, 16)).copy()
+    out = O.bilinear_upsample_nchw(x, 32, 32)
+    assert float(out[0, 0, 16, 16]) == pytest.approx(7.75 + 16 * 7.75, abs=1e-5)
+    # a ramp stays a ramp: interior neighbours differ by 0.5 along x and 8 along y
+    assert np.allclose(np.diff(out[0, 0, 8:24, 8:24], axis=1), 0.5)
+    assert np.allclose(np.diff(out[0, 0, 8:24, 8:24], axis=0), 8.0)
+    assert np.all(out[0, 1:] == out[0, :1])  # every channel the same
