@@ -205,10 +205,23 @@ class UnifiedFPN:
         return _ptr_array([base + 4 * l for l in range(4)])
 
     def forward(self, backbone_features: Sequence[torch.Tensor], return_p6: bool = False,
-                out: Sequence[torch.Tensor] | None = None, input_scales=None):
+                out: Sequence[torch.Tensor] | None = None, input_scales=None,
+                output_fp8: bool = False):
         """P2..P5 (and P6) of the neck; stream-ordered on torch's current stream.
         float8_e4m3fn inputs need ``input_scales`` (4 per-tensor dequantisation scales,
-        floats or 1-element tensors; x = q * scale) and produce bf16 outputs."""
+        floats or 1-element tensors; x = q * scale) and produce bf16 outputs.
+        ``output_fp8`` (16-bit outputs): each level comes back as ``(q, scale)`` for a
+        downstream FP8 consumer -- float8_e4m3fn codes in the output's memory format and one
+        fp32 scale per image (absmax / 448; P ~ q * scale), quantised on the device by the
+        library's quantiser, exactly as ``quantize_fp8(P, per_image=True)``."""
+        if output_fp8:
+            if out is not None:
+                raise ValueError("output_fp8 returns new tensors; out is not supported with it")
+            res = self.forward(backbone_features, return_p6=return_p6, input_scales=input_scales)
+            if res[0].dtype not in (torch.float16, torch.bfloat16):
+                raise ValueError("output_fp8 needs 16-bit outputs (bf16 / fp16 or e4m3 inputs)")
+            from .ops import quantize_fp8
+            return [quantize_fp8(t, per_image=True) for t in res]
         feats, layout, mf = self._prepare(backbone_features)
         if out is not None:
             outs = list(out[:4])

@@ -281,3 +281,30 @@ def test_fp8_two_pass_p2_lateral_is_bitwise_equal(cuda_device, geom):
         _, _, outs[two_pass] = _run_fp8_neck(chans, wts, qf, sc, fpn=fpn)
     for a, b in zip(outs[False], outs[True]):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("fp8_in", [False, True])
+def test_neck_fp8_outputs_for_a_downstream_head(cuda_device, fp8_in):
+    """forward(output_fp8=True): every level as e4m3 codes with per-image scales, bitwise
+    equal to quantising the 16-bit outputs, and within e4m3 rounding of them."""
+    import unified_fpn as U
+    chans, sizes = O.R50_CHANNELS, O.level_sizes(128, 192)
+    feats, wts, qf, sc = _fp8_case(2, chans, sizes, seed=81)
+    fpn = U.UnifiedFPN()
+    fpn.initialize_weights(wts.lat_w, wts.lat_b, wts.out_w, wts.out_b)
+    if fp8_in:
+        xin = [_cl(q.to(E4M3).cuda()) for q in qf]
+        kw = {"input_scales": [float(s) for s in sc]}
+    else:
+        xin = [_cl(f.to(torch.bfloat16).cuda()) for f in feats]
+        kw = {}
+    plain = fpn(xin, return_p6=True, **kw)
+    quant = fpn(xin, return_p6=True, output_fp8=True, **kw)
+    torch.cuda.synchronize()
+    assert len(quant) == 5
+    for p, (q, s) in zip(plain, quant):
+        q_ref, s_ref = U.quantize_fp8(p, per_image=True)
+        assert q.dtype == E4M3 and s.shape == (2,)
+        assert torch.equal(q.view(torch.uint8), q_ref.view(torch.uint8)) and torch.equal(s, s_ref)
+        back = q.float() * s.reshape(-1, 1, 1, 1)
+        assert O.rel_err(back.cpu(), p.float().cpu()) < 0.07  # e4m3: 3 mantissa bits
