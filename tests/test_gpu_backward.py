@@ -95,15 +95,20 @@ def test_p6_backward(cuda_device):
     assert torch.equal(out.cpu().float(), ref.to(torch.bfloat16).float())
 
 
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_neck_backward_matches_autograd(cuda_device, dtype):
-    """Every input, weight and bias gradient of the whole neck (R50 channels, 128x160 image,
-    batch 2, P6 included) against autograd through the oracle neck."""
+@pytest.mark.parametrize("dtype,chans,sizes,batch", [
+    (torch.bfloat16, O.R50_CHANNELS, O.level_sizes(128, 160), 2),
+    (torch.float16, O.R50_CHANNELS, O.level_sizes(128, 160), 2),
+    # Swin-B channels, 1333x800-style sizes: non-2x top-down ratios (13->25->50->100 rows,
+    # 21->42->84->167 columns), ragged tiles, odd P6
+    (torch.float16, O.SWIN_CHANNELS, [(100, 167), (50, 84), (25, 42), (13, 21)], 1),
+])
+def test_neck_backward_matches_autograd(cuda_device, dtype, chans, sizes, batch):
+    """Every input, weight and bias gradient of the whole neck (P6 included) against autograd
+    through the oracle neck."""
     import unified_fpn as U
-    sizes = O.level_sizes(128, 160)
-    fs = O.make_features(2, O.R50_CHANNELS, sizes, seed=21, dist="normal")
-    wts = O.make_weights(O.R50_CHANNELS, seed=22, bias_scale=0.1)
-    neck = U.FPNNeck(O.R50_CHANNELS).to(cuda_device)
+    fs = O.make_features(batch, chans, sizes, seed=21, dist="normal")
+    wts = O.make_weights(chans, seed=22, bias_scale=0.1)
+    neck = U.FPNNeck(chans).to(cuda_device)
     with torch.no_grad():
         for l in range(4):  # the module's fp32 master weights = the oracle's, rounded to dtype
             neck.lateral_w[l].copy_(wts.lat_w[l].to(dtype).float())
