@@ -69,9 +69,12 @@ def test_neck_fp32(cuda_device):
     _neck_case(torch.float32, 1, (64, 128, 256, 256), O.level_sizes(96, 160), "nchw", dist="normal")
 
 
-def test_neck_r50_800x1216_batch2_full_size(cuda_device):
-    """The benchmark workload at full size: R50 FPN neck, 800x1216, batch 2, bf16 NHWC."""
-    fpn, xin, outs = _neck_case(torch.bfloat16, 2, O.R50_CHANNELS, O.level_sizes(800, 1216), "nhwc")
+@pytest.mark.parametrize("dtype,layout", [(torch.bfloat16, "nhwc"), (torch.float16, "nhwc"),
+                                          (torch.bfloat16, "nchw")])
+def test_neck_r50_800x1216_batch2_full_size(cuda_device, dtype, layout):
+    """The benchmark workload at full size: R50 FPN neck, 800x1216, batch 2 (bf16 NHWC as
+    benchmarked; fp16, and NCHW inputs transposed on the device, too)."""
+    fpn, xin, outs = _neck_case(dtype, 2, O.R50_CHANNELS, O.level_sizes(800, 1216), layout)
     # size-independent properties: bitwise determinism and graph replay == direct launch
     again = _run(fpn, xin)
     for a, b in zip(outs, again):
