@@ -524,7 +524,8 @@ struct UnifiedFPNCore::Impl {
     const bool one_stream = prof_events || cfg.single_stream;
     // Programmatic dependent launches measured 2-5% slower on this schedule at the 640x640
     // batch-16 workload (its quantisation kernels release their dependents at their start,
-    // so the next 3x3's CTAs wait on SMs the other streams could use): off.
+    // so the next 3x3's CTAs wait on SMs the other streams could use), and still 1% slower
+    // with the quantisation releasing them at its end: off.
     const bool pdl = false;
     auto opts = [](bool p) {
       ufpn::LaunchOpts o;
