@@ -308,3 +308,30 @@ def test_neck_fp8_outputs_for_a_downstream_head(cuda_device, fp8_in):
         assert torch.equal(q.view(torch.uint8), q_ref.view(torch.uint8)) and torch.equal(s, s_ref)
         back = q.float() * s.reshape(-1, 1, 1, 1)
         assert O.rel_err(back.cpu(), p.float().cpu()) < 0.07  # e4m3: 3 mantissa bits
+
+
+def test_fp8_neck_config5_full_batch(cuda_device):
+    """Config 5 at its full batch on one GPU: FP8 R50 640x640, 128 images (3.4 GB of bf16
+    outputs); the first and last images against the e4m3 oracle (per-tensor input scales of
+    the whole batch, merged maps quantised per image)."""
+    import unified_fpn as U
+    chans, sizes, batch = O.R50_CHANNELS, O.level_sizes(640, 640), 128
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(35)
+    qs = [U.quantize_fp8(torch.randn(batch, c, h, w, device=dev, generator=gen)
+                         .contiguous(memory_format=torch.channels_last))
+          for c, (h, w) in zip(chans, sizes)]
+    wts = O.make_weights(chans, seed=36, bias_scale=0.1)
+    fpn = U.UnifiedFPN()
+    fpn.initialize_weights(wts.lat_w, wts.lat_b, wts.out_w, wts.out_b)
+    outs = fpn([q for q, _ in qs], return_p6=True, input_scales=torch.cat([s for _, s in qs]))
+    torch.cuda.synchronize()
+    assert fpn.device_status() == 0
+    qw = O.quantize_neck_weights(wts)
+    scales = [np.float32(s.item()) for _, s in qs]
+    for n in (0, batch - 1):
+        codes = [q[n:n + 1].float().cpu() for q, _ in qs]  # the e4m3 code values, exactly
+        ref = O.fpn_neck_e4m3(codes, scales, qw)
+        for o, r in zip(outs, ref):
+            assert O.rel_err(o[n:n + 1].float().cpu(), r) < TOL8

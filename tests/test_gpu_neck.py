@@ -323,3 +323,30 @@ def test_neck_large_configs_against_oracle(cuda_device, case):
         _check([o[n:n + 1] for o in outs], ref, TOL16)
         alone = _run(fpn, [x[n:n + 1].contiguous(memory_format=torch.channels_last) for x in xin])
         assert all(torch.equal(a, o[n:n + 1]) for a, o in zip(alone, outs))
+
+
+def test_neck_config3_full_batch_large_offsets(cuda_device):
+    """Config 3 at its full batch on one GPU: R50, 1024x1024, 64 images, bf16 NHWC.  The P2
+    maps hold 2^30 elements (2 GiB), so every address computation must be 64-bit; the first
+    and last images against the oracle, and the last image alone equals its slice bitwise."""
+    import unified_fpn as U
+    chans, sizes, batch = O.R50_CHANNELS, O.level_sizes(1024, 1024), 64
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(33)
+    xin = [_cl(torch.randn(batch, c, h, w, device=dev, generator=gen).to(torch.bfloat16))
+           for c, (h, w) in zip(chans, sizes)]
+    wts = O.make_weights(chans, seed=34, bias_scale=0.1)
+    fpn = U.UnifiedFPN()
+    fpn.initialize_weights(wts.lat_w, wts.lat_b, wts.out_w, wts.out_b)
+    outs = _run(fpn, xin)
+    assert fpn.device_status() == 0
+    rw = O.NeckWeights([O.round_to(w_, torch.bfloat16) for w_ in wts.lat_w], wts.lat_b,
+                       [O.round_to(w_, torch.bfloat16) for w_ in wts.out_w], wts.out_b)
+    for n in (0, batch - 1):
+        ref = O.fpn_neck([x[n:n + 1].float().cpu() for x in xin], rw)
+        _check([o[n:n + 1] for o in outs], ref, TOL16)
+    last = [o[batch - 1:].clone() for o in outs]
+    del outs
+    alone = _run(fpn, [x[batch - 1:].contiguous(memory_format=torch.channels_last) for x in xin])
+    assert all(torch.equal(a, b) for a, b in zip(alone, last))
