@@ -726,6 +726,7 @@ void UnifiedFPNCore::configure_levels(const std::vector<FPNDimensions>& dims, in
   if (dt == DType::E4M3 && lay != Layout::NHWC)
     FPN_THROW("FP8_E4M3 inputs must be NHWC (channels_last)");
   const int N = dims[0].batch_size;
+  if (N <= 0) FPN_THROW("the batch must hold at least one image");
   for (int l = 0; l < 4; ++l) {
     if (dims[l].batch_size != N) FPN_THROW("all levels must share the batch size");
     if (dims[l].channels <= 0 || dims[l].height <= 0 || dims[l].width <= 0)

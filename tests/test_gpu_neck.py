@@ -184,6 +184,12 @@ def test_errors_are_raised_not_exit(cuda_device):
         fpn.set_kernel_config(tile_size=24)
     with pytest.raises(ValueError):
         U.UnifiedFPN(output_channels=128)
+    # an empty batch is refused on the host, before anything is allocated or launched
+    empty = [torch.empty(0, c, 64 >> l, 96 >> l, device="cuda", dtype=torch.bfloat16)
+             .contiguous(memory_format=torch.channels_last) for l, c in enumerate(O.R50_CHANNELS)]
+    with pytest.raises(U.UFPNError):
+        fpn(empty)
+    assert fpn.device_status() == 0
 
 
 @pytest.mark.parametrize("fp8", [False, True])
