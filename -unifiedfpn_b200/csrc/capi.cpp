@@ -283,6 +283,74 @@ int ufpn_core_set_schedule_options(ufpn_core* core, int programmatic_launch, int
   });
 }
 
+namespace {
+// Named integer options of the engine's schedule (ufpn_core_set_option): the field of
+// FPNKernelConfig each name addresses and its accepted values.
+struct OptionField {
+  const char* name;
+  int* (*field)(FPNKernelConfig&);
+  bool (*valid)(int);
+};
+bool valid_bool(int v) { return v == 0 || v == 1; }
+bool valid_ksplit(int v) { return v == 1 || v == 2 || v == 4; }
+const OptionField kOptions[] = {
+    {"ksplit_p3", [](FPNKernelConfig& c) { return &c.lateral_ksplit[1]; }, valid_ksplit},
+    {"ksplit_p4", [](FPNKernelConfig& c) { return &c.lateral_ksplit[2]; }, valid_ksplit},
+    {"ksplit_p5", [](FPNKernelConfig& c) { return &c.lateral_ksplit[3]; }, valid_ksplit},
+};
+// Boolean options (stored as bool in FPNKernelConfig).
+struct BoolOption {
+  const char* name;
+  bool FPNKernelConfig::*field;
+};
+const BoolOption kBoolOptions[] = {
+    {"grouped_topdown", &FPNKernelConfig::grouped_topdown},
+    {"programmatic_launch", &FPNKernelConfig::programmatic_launch},
+    {"chain_priority", &FPNKernelConfig::chain_priority},
+    {"merge_two_levels", &FPNKernelConfig::merge_two_levels},
+    {"single_stream", &FPNKernelConfig::single_stream},
+    {"fused_neck_kernel", &FPNKernelConfig::fused_neck_kernel},
+};
+}  // namespace
+
+int ufpn_core_set_option(ufpn_core* core, const char* name, int value) {
+  if (!core || !name) return fail(UFPN_ERR_INVALID_ARG, "NULL core or name");
+  return guarded([&] {
+    FPNKernelConfig c = core->core.get_kernel_config();
+    for (const auto& o : kOptions) {
+      if (std::strcmp(o.name, name) != 0) continue;
+      if (!o.valid(value)) return fail(UFPN_ERR_INVALID_ARG, std::string("bad value for ") + name);
+      *o.field(c) = value;
+      core->core.set_kernel_config(c);
+      return UFPN_OK;
+    }
+    for (const auto& o : kBoolOptions) {
+      if (std::strcmp(o.name, name) != 0) continue;
+      if (!valid_bool(value)) return fail(UFPN_ERR_INVALID_ARG, std::string("bad value for ") + name);
+      c.*o.field = value != 0;
+      core->core.set_kernel_config(c);
+      return UFPN_OK;
+    }
+    return fail(UFPN_ERR_INVALID_ARG, std::string("unknown option ") + name);
+  });
+}
+
+int ufpn_core_get_option(const ufpn_core* core, const char* name, int* value) {
+  if (!core || !name || !value) return fail(UFPN_ERR_INVALID_ARG, "NULL argument");
+  FPNKernelConfig c = core->core.get_kernel_config();
+  for (const auto& o : kOptions)
+    if (std::strcmp(o.name, name) == 0) {
+      *value = *o.field(c);
+      return UFPN_OK;
+    }
+  for (const auto& o : kBoolOptions)
+    if (std::strcmp(o.name, name) == 0) {
+      *value = (c.*o.field) ? 1 : 0;
+      return UFPN_OK;
+    }
+  return fail(UFPN_ERR_INVALID_ARG, std::string("unknown option ") + name);
+}
+
 size_t ufpn_core_get_memory_usage(const ufpn_core* core) {
   return core ? core->core.get_memory_usage() : 0;
 }

@@ -108,6 +108,13 @@ struct UnifiedFPNCore::Impl {
   // each tile while it writes M4, so L4 cannot be merged in place); null: merge per level.
   void* lat4_raw = nullptr;
   void* wb_table = nullptr;   // P2 lateral's precomputed top-down (bilinear) weights
+  // Split-K grouped laterals: fp32 partials per level and per-tile arrival counters (one
+  // allocation: counters first), sized for split_alloc[l] units per tile.
+  float* split_part[4] = {};
+  int* split_sem = nullptr;
+  int split_sem_off[4] = {};
+  int split_alloc[4] = {1, 1, 1, 1};
+  size_t split_bytes = 0;
   const float* in_scale[4] = {};  // e4m3: scales of the current forward's inputs
   unsigned* fp8_amax = nullptr;   // e4m3: [4][N] per-image absmax of M_l (fp32 bits)
   float* fp8_scale = nullptr;     // e4m3: [4][N] per-image dequantisation scale of M_l
@@ -173,7 +180,58 @@ struct UnifiedFPNCore::Impl {
     lat4_raw = nullptr;
     cudaFree(wb_table);
     wb_table = nullptr;
+    free_split();
     workspace_bytes = 0;
+  }
+  void free_split() {
+    cudaFree(split_sem);  // one allocation with the partials
+    split_sem = nullptr;
+    for (int l = 0; l < 4; ++l) {
+      split_part[l] = nullptr;
+      split_alloc[l] = 1;
+    }
+    workspace_bytes -= split_bytes;
+    split_bytes = 0;
+  }
+  // Units per tile of level l's lateral in the grouped launch (1 when the level does not
+  // split or its K loop is too short for the configured split).
+  int lateral_ksplit(int l) const {
+    if (l < 1 || l > 3) return 1;
+    const int ks = cfg.lateral_ksplit[l];
+    const int kbs = (cin[l] + 63) / 64;
+    return (ks == 2 || ks == 4) && kbs >= ks ? ks : 1;
+  }
+  // Allocates (before any capture) the split-K workspace the current configuration needs.
+  void ensure_split_workspace() {
+    if (!tensor_core_path() || dtype == DType::E4M3) return;
+    bool same = split_sem != nullptr || (lateral_ksplit(1) == 1 && lateral_ksplit(2) == 1 &&
+                                         lateral_ksplit(3) == 1);
+    for (int l = 1; l < 4 && same && split_sem; ++l) same = split_alloc[l] == lateral_ksplit(l);
+    if (same) return;
+    release_graphs();
+    free_split();
+    size_t sem_ints = 0, part_bytes = 0;
+    size_t off[4] = {};
+    for (int l = 1; l < 4; ++l) {
+      const ufpn::Conv3x3Tiling t = ufpn::default_tiling(H[l], W[l]);
+      split_sem_off[l] = static_cast<int>(sem_ints);
+      sem_ints += static_cast<size_t>(ufpn::neck_lateral_tiles(batch, H[l], W[l], t));
+      off[l] = part_bytes;
+      part_bytes += ufpn::neck_split_part_bytes(batch, H[l], W[l], t, lateral_ksplit(l));
+    }
+    const size_t sem_bytes = (sem_ints * sizeof(int) + 255) / 256 * 256;
+    void* p = nullptr;
+    check(cudaMalloc(&p, sem_bytes + part_bytes), "workspace");
+    check(cudaMemset(p, 0, sem_bytes), "workspace");
+    split_sem = static_cast<int*>(p);
+    for (int l = 1; l < 4; ++l) {
+      split_alloc[l] = lateral_ksplit(l);
+      split_part[l] = split_alloc[l] > 1
+                          ? reinterpret_cast<float*>(static_cast<char*>(p) + sem_bytes + off[l])
+                          : nullptr;
+    }
+    split_bytes = sem_bytes + part_bytes;
+    workspace_bytes += split_bytes;
   }
   void free_weights() {
     for (int l = 0; l < 4; ++l) {
@@ -432,7 +490,14 @@ struct UnifiedFPNCore::Impl {
     // With lat4_raw: L4 goes there and ONE launch merges M4 and M3 (merge_two_levels).
     const bool two_level = lat4_raw != nullptr && cfg.merge_two_levels;
     if (two_level) lv[2].merged = lat4_raw;
-    const ufpn::NeckJobSpec grouped[3] = {{0, 3, 0}, {0, 2, 0}, {0, 1, 0}};
+    // grouped_topdown: the grouped launch writes M5, M4, M3 itself (no merge kernels).
+    const int td = cfg.grouped_topdown && !two_level ? 1 : 0;
+    for (int l = 1; l < 4; ++l) {
+      lv[l].split_part = split_part[l];
+      lv[l].split_sem = split_sem ? split_sem + split_sem_off[l] : nullptr;
+    }
+    auto ks = [&](int l) { return split_part[l] ? split_alloc[l] : 1; };
+    const ufpn::NeckJobSpec grouped[3] = {{0, 3, 0, ks(3)}, {0, 2, td, ks(2)}, {0, 1, td, ks(1)}};
     ufpn::NeckPlan gplan;
     check(ufpn::plan_neck_jobs(gplan, dtype, batch, lv, nullptr, grouped, 3, d_sched, d_status, 0,
                                trace_next ? d_trace : nullptr),
@@ -441,7 +506,17 @@ struct UnifiedFPNCore::Impl {
     if (prof_events) cudaEventRecord(prof[1], main);
     conv_level(3);
     if (prof_events) cudaEventRecord(prof[2], main);
-    if (two_level) {
+    if (td) {
+      // M4 and M3 are complete: no merge stages (their profile slots stay empty).
+      if (prof_events) cudaEventRecord(prof[3], main);
+      conv_level(2);
+      if (prof_events) {
+        cudaEventRecord(prof[4], main);
+        cudaEventRecord(prof[5], main);
+      }
+      conv_level(1);
+      if (prof_events) cudaEventRecord(prof[6], main);
+    } else if (two_level) {
       ok(ufpn::launch_merge_two_levels(dtype, merged[3], lat4_raw, merged[2], merged[1],
                                        merged[1], batch, H[3], W[3], H[2], W[2], H[1], W[1],
                                        main, nullptr, nullptr, nullptr, chain),
@@ -898,6 +973,7 @@ void UnifiedFPNCore::forward_raw_scaled(const void* const* in, const float* cons
   }
   DeviceGuard g(m.device);
   m.ensure_weight_packing();
+  m.ensure_split_workspace();
   if (m.profiling) {
     const int n = m.enqueue(in, out, p6, stream, true);
     m.check(cudaEventRecord(m.prof[9], stream), "event");
@@ -1039,8 +1115,18 @@ int UnifiedFPNCore::device_status(bool reset) {
   CUDA_CHECK(cudaDeviceSynchronize());
   CUDA_CHECK(cudaMemcpy(&v, impl_->d_status, sizeof(int), cudaMemcpyDeviceToHost));
   if (reset) CUDA_CHECK(cudaMemset(impl_->d_status, 0, sizeof(int)));
-  // After a pipeline abort, make sure the neck kernel's schedule counters start at zero.
-  if (reset && v != 0) CUDA_CHECK(cudaMemset(impl_->d_sched, 0, 64 * sizeof(int)));
+  // After a pipeline abort, make sure the neck kernel's schedule counters (and the split-K
+  // arrival counters) start at zero.
+  if (reset && v != 0) {
+    CUDA_CHECK(cudaMemset(impl_->d_sched, 0, 64 * sizeof(int)));
+    if (impl_->split_sem) {
+      size_t n = 0;
+      for (int l = 1; l < 4; ++l)
+        n += static_cast<size_t>(ufpn::neck_lateral_tiles(
+            impl_->batch, impl_->H[l], impl_->W[l], ufpn::default_tiling(impl_->H[l], impl_->W[l])));
+      CUDA_CHECK(cudaMemset(impl_->split_sem, 0, n * sizeof(int)));
+    }
+  }
   return v;
 }
 

@@ -18,6 +18,16 @@
 // for work that a resident CTA has taken: the schedule cannot deadlock, even
 // if not all CTAs are resident.  Every wait is still bounded (ptx.cuh).
 //
+// Split-K lateral tiles (job.ksplit > 1): a tile with a long K loop (the P5 lateral's
+// 2048 input channels are 32 k-blocks; one 128-pixel tile would hold its SM for its whole
+// weight stream) is cut into ksplit units over consecutive k-block ranges, numbered
+// consecutively so that idle CTAs take them side by side.  Every unit writes its fp32
+// partial accumulator to the job's workspace and counts itself on the tile's semaphore; the
+// unit that arrives last sums the partials pairwise, p0 + p1 or (p0 + p1) + (p2 + p3) (its
+// own part comes from TMEM, bitwise equal to what it wrote), and runs the tile's real
+// epilogue.  Each add is commutative, so the bits do not depend on which unit arrives last:
+// results are deterministic.  The last unit resets the semaphore for the next launch.
+//
 // Cross-CTA visibility: an epilogue waits for its own TMA stores to complete
 // (cp.async.bulk.wait_group 0), fences the async proxy, synchronises the
 // epilogue warps and publishes with a release add; consumers acquire the
@@ -66,6 +76,10 @@ struct NeckJob {
   int publish;             // lateral: a later job of this launch waits on this level
   int act;                 // conv3x3: output activation after the bias (0 = none)
   float act_alpha;
+  int ksplit;              // lateral: units per tile over K (1 = whole tiles)
+  int kb_per;              // k-blocks per unit (the last unit of a tile may have fewer)
+  float* part;             // ksplit > 1: fp32 partials, [unit][256 columns][128 rows]
+  int* sem;                // ksplit > 1: per-tile arrival counters (zero between launches)
 };
 
 struct NeckParams {
@@ -141,6 +155,30 @@ __device__ __forceinline__ int neck_find_job(const NeckParams& p, int t) {
   return j;
 }
 
+// Unit `local` of a job -> its pixel tile and (split-K jobs) its part of the K loop.
+__device__ __forceinline__ int neck_unit_tile(const NeckJob& jb, int local, int& part) {
+  if (jb.ksplit <= 1) {
+    part = 0;
+    return local;
+  }
+  const int pt = local / jb.ksplit;
+  part = local - pt * jb.ksplit;
+  return pt;
+}
+__device__ __forceinline__ void neck_unit_kb(const NeckJob& jb, int part, int& kb0, int& kb1) {
+  kb0 = part * jb.kb_per;
+  kb1 = jb.ksplit <= 1 ? jb.num_kb : min(jb.num_kb, kb0 + jb.kb_per);
+}
+__device__ __forceinline__ int atom_acq_rel_gpu_add(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
+               : "memory");
+  return old;
+}
+__device__ __forceinline__ void fence_acq_rel_gpu() {
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+}
+
 __device__ __forceinline__ void neck_tile_origin(const NeckJob& jb, int local, int& n, int& x0,
                                                  int& y0) {
   const int tx = local % jb.tiles_x;
@@ -185,6 +223,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   int* ring = reinterpret_cast<int*>(rempty_bar + R);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ring + R);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* split_last = abort_flag + 1;  // epilogue leader -> epilogue: last unit of a tile
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -252,8 +291,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (t >= P.total_tiles) break;
         const int j = neck_find_job(P, t);
         const NeckJob& jb = P.jobs[j];
-        int n, x0, y0;
-        neck_tile_origin(jb, t - jb.tile_start, n, x0, y0);
+        int n, x0, y0, part, kb0, kb1;
+        neck_tile_origin(jb, neck_unit_tile(jb, t - jb.tile_start, part), n, x0, y0);
+        neck_unit_kb(jb, part, kb0, kb1);
         if (jb.mode == 1 && jb.dep_level >= 0 && !(ready_level_mask & (1 << jb.dep_level))) {
           if (!wait_counter(&sched[1 + jb.dep_level], jb.dep_count, abort_flag, P.status,
                             kDevTimeoutDependency)) {
@@ -263,7 +303,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           fence_proxy_async_all();
           ready_level_mask |= 1 << jb.dep_level;
         }
-        for (int kb = 0; kb < jb.num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, P.status,
                          kDevTimeoutProducer)) {
             ok = false;
@@ -281,7 +321,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                       x0 + dx, y0 + dy, n, jb.mode == 0 ? kPolicyEvictFirst : kPolicyEvictLast);
           tma_load_2d(smem_b + stage * kTcBStage, &jb.map_b, &full_bar[stage], kb * kTcBlockK, 0,
                       kPolicyEvictLast);
-          if (kb == jb.num_kb - 1) t_next = atomicAdd(&sched[0], 1);
+          if (kb == kb1 - 1) t_next = atomicAdd(&sched[0], 1);
           ++issued;
           if (++stage == S) {
             stage = 0;
@@ -326,7 +366,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         if (t < 0) break;
         const NeckJob& jm = P.jobs[neck_find_job(P, t)];
-        const int num_kb = jm.num_kb;
+        int mpart, kb0, kb1;
+        neck_unit_tile(jm, t - jm.tile_start, mpart);
+        neck_unit_kb(jm, mpart, kb0, kb1);
+        const int num_kb = kb1 - kb0;
         if (P.trace && jm.mode == 1 && jm.level == 0 && t == jm.tile_start)
           P.trace[6] = globaltimer_ns();
         if (!mbar_wait(&acce_bar[acc], acc_phase ^ 1u, abort_flag, P.status, kDevTimeoutMma))
@@ -379,9 +422,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     int ready_level_mask = 0;   // leader: dependency levels observed complete
     bool ok = true;
 
-    // Leader: make sure level `lvl` laterals are complete (acquire), then load the
-    // coarse box of lateral tile `t` of job `jb`.
-    auto request_coarse = [&](const NeckJob& jb, int t) -> bool {
+    // Leader: make sure the coarser level's laterals (the top-down input of lateral job jb)
+    // are complete (acquire).
+    auto wait_dep = [&](const NeckJob& jb) -> bool {
       if (!(ready_level_mask & (1 << (jb.level + 1)))) {
         if (!wait_counter(&sched[1 + jb.level + 1], jb.dep_count, abort_flag, P.status,
                           kDevTimeoutDependency))
@@ -389,6 +432,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         fence_proxy_async_all();
         ready_level_mask |= 1 << (jb.level + 1);
       }
+      return true;
+    };
+    // Leader: wait_dep, then load the coarse box of lateral tile `t` of job `jb`.
+    auto request_coarse = [&](const NeckJob& jb, int t) -> bool {
+      if (!wait_dep(jb)) return false;
       if (jb.cbox_w > 0) {
         int n, x0, y0;
         neck_tile_origin(jb, t - jb.tile_start, n, x0, y0);
@@ -418,7 +466,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const bool lateral = jb.mode == 0;
       const bool has_coarse = lateral && jb.coarse != nullptr;
       const bool staged = has_coarse && jb.cbox_w > 0;
-      if (has_coarse && leader && coarse_requested != t) ok = request_coarse(jb, t);
+      const bool split = lateral && jb.ksplit > 1;  // (split jobs never stage a coarse box)
+      int part = 0;
+      const int ptile = neck_unit_tile(jb, t - jb.tile_start, part);
+      if (has_coarse && !split && leader && coarse_requested != t) ok = request_coarse(jb, t);
       bool wok = mbar_wait(&accf_bar[acc], acc_phase, abort_flag, P.status, kDevTimeoutEpilogue);
       if (staged && wok && ok)
         wok = mbar_wait(cfull_bar, cphase, abort_flag, P.status, kDevTimeoutEpilogue);
@@ -427,8 +478,78 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (!epi_vote_all(wok && ok)) break;
       tc_fence_after();
 
+      // Split-K unit: write the fp32 partial ([unit][column][row]: a warp stores 128
+      // contiguous bytes per column), count the arrival; only the tile's last unit goes on.
+      bool final_unit = true;
+      if (split) {
+        float* mine = jb.part + static_cast<size_t>(t - jb.tile_start) * (kTcBlockN * kTcBlockM);
+        const uint32_t tacc = tmem_base + static_cast<uint32_t>(acc * kTcBlockN + chalf * 128) +
+                              (static_cast<uint32_t>(quarter * 32) << 16);
+#pragma unroll 1
+        for (int h = 0; h < 4; ++h) {  // this warp's 128 columns, 32 at a time
+          uint32_t r[32];
+          __syncwarp();
+          tmem_ld32(tacc + h * 32, r);
+          tmem_wait_ld();
+          float* dst = mine + static_cast<size_t>(chalf * 128 + h * 32) * kTcBlockM + row;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) __stcg(dst + static_cast<size_t>(i) * kTcBlockM, __uint_as_float(r[i]));
+        }
+        __threadfence();
+        epi_bar_sync();
+        if (leader) {
+          const int before = atom_acq_rel_gpu_add(&jb.sem[ptile], 1);
+          const int last = before == jb.ksplit - 1;
+          if (last) jb.sem[ptile] = 0;  // every unit of the tile has arrived: reset for the next launch
+          *split_last = last;
+        }
+        epi_bar_sync();
+        final_unit = *split_last != 0;  // uniform
+        if (final_unit) {
+          fence_acq_rel_gpu();  // the other units' partials (published before their arrival)
+          // Pairwise sum p0 + p1 (ksplit 2) or (p0 + p1) + (p2 + p3) (ksplit 4): every add
+          // is commutative, so starting from its own part (in TMEM, bitwise what it wrote)
+          // any unit computes the same bits.  Written back into the accumulator so the
+          // epilogue below runs unchanged.
+          const float* base = jb.part +
+                              static_cast<size_t>(ptile) * jb.ksplit * (kTcBlockN * kTcBlockM) +
+                              static_cast<size_t>(chalf * 128) * kTcBlockM + row;
+          const int partner = part ^ 1;
+          const int other0 = (part ^ 2) & ~1;  // ksplit 4: the other pair
+#pragma unroll 1
+          for (int h = 0; h < 4; ++h) {
+            uint32_t r[32];
+            __syncwarp();
+            tmem_ld32(tacc + h * 32, r);
+            tmem_wait_ld();
+            const float* ph = base + static_cast<size_t>(h * 32) * kTcBlockM;
+            const float* pp = ph + static_cast<size_t>(partner) * (kTcBlockN * kTcBlockM);
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              r[i] = __float_as_uint(__uint_as_float(r[i]) +
+                                     __ldcg(pp + static_cast<size_t>(i) * kTcBlockM));
+            if (jb.ksplit == 4) {
+              const float* p0 = ph + static_cast<size_t>(other0) * (kTcBlockN * kTcBlockM);
+              const float* p1 = p0 + static_cast<size_t>(kTcBlockN) * kTcBlockM;
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                r[i] = __float_as_uint(__uint_as_float(r[i]) +
+                                       (__ldcg(p0 + static_cast<size_t>(i) * kTcBlockM) +
+                                        __ldcg(p1 + static_cast<size_t>(i) * kTcBlockM)));
+            }
+            tmem_st32(tacc + h * 32, r);
+          }
+          tmem_wait_st();
+          if (has_coarse && leader) ok = wait_dep(jb);
+          if (!epi_vote_all(ok)) break;
+        } else {
+          tc_fence_before();
+          mbar_arrive(&acce_bar[acc]);  // this unit's accumulator is fully read
+        }
+      }
+      if (final_unit) {
       int n, x0, y0;
-      neck_tile_origin(jb, t - jb.tile_start, n, x0, y0);
+      neck_tile_origin(jb, ptile, n, x0, y0);
       const int tw = jb.tile_w;
       const int py = y0 + row / tw;
       const int px = x0 + row % tw;
@@ -585,6 +706,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       if (P.trace && lateral && !jb.publish && leader)
         atomicMax(&P.trace[1 + jb.level], globaltimer_ns());  // stores issued, not complete
+      }  // final_unit
       // The coarse buffer is free (lateral tiles passed the barrier above; other
       // tiles do not read it): prefetch the next tile's coarse box if that tile is
       // a lateral with a top-down add.
@@ -593,7 +715,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const int tn = ring[rslot];
           if (tn >= 0) {
             const NeckJob& jn = P.jobs[neck_find_job(P, tn)];
-            if (jn.mode == 0 && jn.coarse != nullptr) ok = request_coarse(jn, tn);
+            if (jn.mode == 0 && jn.coarse != nullptr && jn.ksplit <= 1)
+              ok = request_coarse(jn, tn);
           }
         }
       }

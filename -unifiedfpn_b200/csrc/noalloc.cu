@@ -22,8 +22,13 @@
 // Host code must not pass the array's name to a kernel: in host code it names a
 // host-side stand-in, not device memory.  The device address is obtained with
 // cudaGetSymbolAddress the first time the entry point runs on a device (with
-// that device current) and cached; that first call therefore performs a
-// runtime query and should come before any stream capture.
+// that device current) and cached together with the identity of the device's
+// context; that first call therefore performs a runtime query and should come
+// before any stream capture.  If the context is replaced (cudaDeviceReset, or
+// any teardown of the primary context), the module is loaded again at a new
+// address: the next call sees the new context identity and looks it up again.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <cstdio>
@@ -43,19 +48,49 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 
 std::mutex g_addr_mu;
 void* g_addr[64] = {};
+unsigned long long g_ctx_id[64] = {};  // context the cached address belongs to (0 = none)
 
-// Device address of g_noalloc_scratch on the current device (queried once per device).
+// Unique id of the calling thread's current context (ids are never reused within a
+// process), or 0 when no context is current yet or the driver lacks the query.
+unsigned long long current_context_id() {
+  static PFN_cuCtxGetCurrent_v4000 get_current = nullptr;
+  static PFN_cuCtxGetId_v12000 get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 4000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(p);
+  });
+  if (!get_current || !get_id) return 0;
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  unsigned long long id = 0;
+  return get_id(ctx, &id) == CUDA_SUCCESS ? id : 0;
+}
+
+// Device address of g_noalloc_scratch on the current device: looked up once per device and
+// context (the set-up step), then served from the cache.
 cudaError_t scratch_address(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lk(g_addr_mu);
-  if (!g_addr[dev]) {
+  const unsigned long long ctx = current_context_id();
+  if (!g_addr[dev] || ctx == 0 || ctx != g_ctx_id[dev]) {
     void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);  // creates the context if needed
     if (e != cudaSuccess) return e;
     g_addr[dev] = p;
+    g_ctx_id[dev] = current_context_id();
   }
   *out = g_addr[dev];
   return cudaSuccess;
@@ -95,6 +130,8 @@ extern "C" int ufpn_neck_forward_noalloc(
       return fail(UFPN_ERR_INVALID_ARG, "NULL tensor pointer");
     if (in_channels[l] <= 0 || in_channels[l] % 8 != 0 || heights[l] <= 0 || widths[l] <= 0)
       return fail(UFPN_ERR_INVALID_ARG, "need Cin % 8 == 0 and positive sizes");
+    if (l < 3 && (heights[l + 1] > heights[l] || widths[l + 1] > widths[l]))
+      return fail(UFPN_ERR_INVALID_ARG, "levels must be ordered fine (C2) to coarse (C5)");
     off[l] = round_up(need, 256);
     need = off[l] + static_cast<size_t>(batch) * heights[l] * widths[l] * 256 * 2;
   }
@@ -115,8 +152,10 @@ extern "C" int ufpn_neck_forward_noalloc(
   int* own_status = reinterpret_cast<int*>(s + kCountersBytes);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // The array keeps the previous call's contents: the schedule counters and the
-  // status word must start at zero.
+  // status word must start at zero.  A caller-owned status word is cleared as well, so that
+  // it reports this call alone.
   e = cudaMemsetAsync(s, 0, kCountersBytes + kStatusBytes, st);
+  if (e == cudaSuccess && status) e = cudaMemsetAsync(status, 0, sizeof(int), st);
   if (e != cudaSuccess)
     return fail(UFPN_ERR_CUDA, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
   ufpn::NeckLevel lv[4];

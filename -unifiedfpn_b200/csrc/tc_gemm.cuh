@@ -105,7 +105,9 @@ struct TcCfgT {
   static constexpr int kOffB = kStages * kTcAStage;
   static constexpr int kOffStaging = kOffB + kStages * kTcBStage;
   static constexpr int kOffBars = kOffStaging + kStageBufs * kEpiWarps * kTcStagingPerWarp;
-  static constexpr int kSmemBytes = kOffBars + 256 + 1024 /*alignment slack*/;
+  // the tile's 256 fp32 biases, staged once per CTA (16-bit lateral without channel slices)
+  static constexpr int kOffBias = kOffBars + 256;
+  static constexpr int kSmemBytes = kOffBias + 1024 + 1024 /*alignment slack*/;
 };
 static_assert(TcCfgT<0, __nv_fp8_e4m3>::kSmemBytes <= 232448 &&
                   TcCfgT<0, __nv_bfloat16>::kSmemBytes <= 232448 &&
@@ -387,13 +389,16 @@ __global__ void __launch_bounds__(32) tc_wb_table_kernel(const TcGemmArgs a, uin
 // and 2u + 1 (rank 1; past the last tile it is a virtual, all-padding tile that is
 // computed but never stored), and each warp releases its accumulator on the pair
 // leader's barrier (shared::cluster address leader_acce).
+// bias_s (optional): the 256 biases staged in shared memory (read there instead of from
+// global memory every tile; the epilogue's latency chain is its per-tile cost).
 template <int kMode, typename T, bool kPair = false, int kStageBufs = 1,
           int kEpiW = kTcEpiWarps>
 __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtensorMap* map_out,
                                             uint32_t tmem_base, uint64_t* accf_bar,
                                             uint64_t* acce_bar, uint8_t* smem_stage,
                                             volatile int* abort_flag, int warp, int lane,
-                                            bool bil_mma, uint32_t leader_acce = 0) {
+                                            bool bil_mma, uint32_t leader_acce = 0,
+                                            const float* bias_s = nullptr) {
   using O = typename TcElem<T>::Out;
   constexpr bool kFp8 = TcElem<T>::kFp8;
   // kEpiW / 4 warps share each TMEM lane quarter; each owns kChans output channels,
@@ -479,30 +484,48 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
       const int col0 = chalf * kChans + step * 64;
       const uint32_t taddr = tmem_base + static_cast<uint32_t>(acc * kTcBlockN + col0) +
                              (static_cast<uint32_t>(quarter * 32) << 16);
+      // With 8 epilogue warps (registers to spare), both 32-column halves of the step are
+      // loaded from TMEM with one wait: the loads overlap each other and the staging-buffer
+      // wait below (per-tile timestamps of the lateral showed its epilogue bound by serial
+      // TMEM round trips).  16 warps (at most 112 registers each) load a half at a time.
+      constexpr bool kBoth = kEpiW <= 8;
+      uint32_t rr[kBoth ? 64 : 32];
+      auto release_acc = [&] {
+        // All of this tile's accumulator columns for this warp are in registers:
+        // hand the TMEM buffer back to the MMA warp before the memory work.
+        tc_fence_before();
+        if constexpr (kPair) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(leader_acce + static_cast<uint32_t>(acc) * 8u);
+        } else {
+          mbar_arrive(&acce_bar[acc]);
+        }
+      };
+      if constexpr (kBoth) {
+        __syncwarp();
+        tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&rr[0]));
+        tmem_ld32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&rr[32]));
+      }
       // The TMA store that last read this staging buffer must be done with it (the e4m3
       // row of a tile is assembled from both steps, so it is only waited for at step 0).
       if (omode == 0 || (omode == 2 && step == 0)) {
         if (lane == 0) bulk_wait_group_read<kStageBufs - 1>();
       }
       const uint32_t stage_addr = smem_u32(my_stage + sbuf * kTcStagingPerWarp);
-      // Two 32-column halves per 64-channel step (half the live registers).
-#pragma unroll 1
+      if constexpr (kBoth) {
+        tmem_wait_ld();
+        if (step == kSteps - 1) release_acc();
+      }
+      // Two 32-column halves per 64-channel step.
+#pragma unroll
       for (int half = 0; half < 2; ++half) {
         const int c0 = col0 + half * 32;
-        uint32_t r[32];
-        __syncwarp();
-        tmem_ld32(taddr + half * 32, r);
-        tmem_wait_ld();
-        if (step == kSteps - 1 && half == 1) {
-          // All of this tile's accumulator columns for this warp are in registers:
-          // hand the TMEM buffer back to the MMA warp before the memory work.
-          tc_fence_before();
-          if constexpr (kPair) {
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(leader_acce + static_cast<uint32_t>(acc) * 8u);
-          } else {
-            mbar_arrive(&acce_bar[acc]);
-          }
+        const uint32_t* r = kBoth ? rr + half * 32 : rr;
+        if constexpr (!kBoth) {
+          __syncwarp();
+          tmem_ld32(taddr + half * 32, *reinterpret_cast<uint32_t(*)[32]>(&rr[0]));
+          tmem_wait_ld();
+          if (step == kSteps - 1 && half == 1) release_acc();
         }
         float v[32];
         const float4* b4 = reinterpret_cast<const float4*>(args.bias + scol + c0);
@@ -518,9 +541,10 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
             v[4 * i + 3] = fmaf(__uint_as_float(r[4 * i + 3]), ascale * ss.w, bb.w);
           }
         } else {
+          const float4* bs4 = bias_s ? reinterpret_cast<const float4*>(bias_s + c0) : nullptr;
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            const float4 bb = __ldg(b4 + i);
+            const float4 bb = bs4 ? bs4[i] : __ldg(b4 + i);
             v[4 * i + 0] = __uint_as_float(r[4 * i + 0]) + bb.x;
             v[4 * i + 1] = __uint_as_float(r[4 * i + 1]) + bb.y;
             v[4 * i + 2] = __uint_as_float(r[4 * i + 2]) + bb.z;
@@ -647,6 +671,9 @@ __global__ void __launch_bounds__(TcCfgT<kMode, T>::kThreads, 1)
   uint64_t* done_bar = acce_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* bias_s = reinterpret_cast<float*>(smem + Cfg::kOffBias);
+  // (16-bit laterals with one 256-channel output slice read their biases from shared memory)
+  const bool stage_bias = kMode == 0 && !TcElem<T>::kFp8 && args.slices <= 1;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -831,8 +858,15 @@ __global__ void __launch_bounds__(TcCfgT<kMode, T>::kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    tc_epilogue<kMode, T, false, Cfg::kStageBufs, Cfg::kEpiWarps>(args, &map_out, tmem_base, accf_bar, acce_bar, smem_stage,
-                          abort_flag, warp, lane, bil_mma);
+    if (stage_bias) {
+      // (after griddep_wait: the biases may come from the kernel before this one)
+      for (int i = threadIdx.x - 64; i < kTcBlockN; i += Cfg::kEpiWarps * 32)
+        bias_s[i] = __ldg(args.bias + i);
+      asm volatile("bar.sync 1, %0;" ::"r"(Cfg::kEpiWarps * 32) : "memory");
+    }
+    tc_epilogue<kMode, T, false, Cfg::kStageBufs, Cfg::kEpiWarps>(
+        args, &map_out, tmem_base, accf_bar, acce_bar, smem_stage, abort_flag, warp, lane,
+        bil_mma, 0, stage_bias ? bias_s : nullptr);
   }
 
   tc_fence_before();

@@ -504,6 +504,16 @@ bool tc_attach_wb_table(TcPlan& plan, const void* table) {
 
 static_assert(sizeof(NeckParams) <= sizeof(NeckPlan::params), "NeckPlan::params too small");
 
+int neck_lateral_tiles(int N, int H, int W, Conv3x3Tiling t) {
+  if (!valid_tiling(t) || N <= 0 || H <= 0 || W <= 0) return 0;
+  return ((W + t.tile_w - 1) / t.tile_w) * ((H + t.tile_h - 1) / t.tile_h) * N;
+}
+
+size_t neck_split_part_bytes(int N, int H, int W, Conv3x3Tiling t, int ksplit) {
+  return static_cast<size_t>(neck_lateral_tiles(N, H, W, t)) * (ksplit > 1 ? ksplit : 0) *
+         kTcBlockM * kTcBlockN * sizeof(float);
+}
+
 cudaError_t plan_neck_jobs(NeckPlan& plan, DType dt, int N, const NeckLevel* lv, void* p6,
                            const NeckJobSpec* specs, int num_specs, int* sched, int* status,
                            int max_ctas, unsigned long long* trace) {
@@ -524,6 +534,11 @@ cudaError_t plan_neck_jobs(NeckPlan& plan, DType dt, int N, const NeckLevel* lv,
     if (s.mode == 0) {
       if (L.Cin <= 0 || L.Cin % 8 != 0 || !aligned16(L.lat_b)) return cudaErrorInvalidValue;
       if (lat_in_launch[s.level]) return cudaErrorInvalidValue;
+      if (s.ksplit != 1 && s.ksplit != 2 && s.ksplit != 4) return cudaErrorInvalidValue;
+      const int cin_blocks = (L.Cin + kTcBlockK - 1) / kTcBlockK;
+      if (s.ksplit > 1 && (cin_blocks < s.ksplit || !L.split_part || !L.split_sem ||
+                           !aligned16(L.split_part)))
+        return cudaErrorInvalidValue;
       lat_in_launch[s.level] = true;
       lat_tiles[s.level] = ((L.W + t.tile_w - 1) / t.tile_w) * ((L.H + t.tile_h - 1) / t.tile_h) * N;
     } else if (!aligned16(L.out) || !aligned16(L.conv_b)) {
@@ -560,6 +575,18 @@ cudaError_t plan_neck_jobs(NeckPlan& plan, DType dt, int N, const NeckLevel* lv,
       J.cin_blocks = (L.Cin + kTcBlockK - 1) / kTcBlockK;
       J.num_kb = J.cin_blocks;
       J.bias = L.lat_b;
+      J.ksplit = specs[j].ksplit;
+      if (J.ksplit > 1) {
+        // ceil(num_kb / ksplit) k-blocks per unit; every unit gets at least one
+        J.kb_per = (J.num_kb + J.ksplit - 1) / J.ksplit;
+        while ((J.ksplit - 1) * J.kb_per >= J.num_kb) --J.kb_per;  // (never below 1: checked)
+        J.part = L.split_part;
+        J.sem = L.split_sem;
+        start += J.num_tiles * (J.ksplit - 1);  // units = tiles x ksplit
+        J.num_tiles *= J.ksplit;
+      } else {
+        J.kb_per = J.num_kb;
+      }
       if ((e = encode_nhwc(&J.map_a, dt, L.x, N, L.H, L.W, L.Cin, t.tile_w, t.tile_h)) !=
           cudaSuccess)
         return e;
@@ -579,7 +606,8 @@ cudaError_t plan_neck_jobs(NeckPlan& plan, DType dt, int N, const NeckLevel* lv,
         J.dep_count = lat_in_launch[l + 1] ? lat_tiles[l + 1] : 0;
         const int ch = static_cast<int>(std::ceil((t.tile_h - 1) * J.scale_y)) + 2;
         const int cw = static_cast<int>(std::ceil((t.tile_w - 1) * J.scale_x)) + 2;
-        if (ch * cw <= kTcCoarseMaxPix && ch <= 256 && cw <= 256) {
+        // (split-K tiles read their taps from global memory in the last unit's epilogue)
+        if (J.ksplit <= 1 && ch * cw <= kTcCoarseMaxPix && ch <= 256 && cw <= 256) {
           J.cbox_h = ch;
           J.cbox_w = cw;
           if ((e = encode_nhwc(&J.map_coarse, dt, C.merged, N, C.H, C.W, kTcBlockN, cw, ch)) !=
@@ -590,6 +618,8 @@ cudaError_t plan_neck_jobs(NeckPlan& plan, DType dt, int N, const NeckLevel* lv,
     } else {
       J.cin_blocks = kTcBlockN / kTcBlockK;
       J.num_kb = 9 * J.cin_blocks;
+      J.kb_per = J.num_kb;
+      J.ksplit = 1;
       J.bias = L.conv_b;
       if (L.act < 0 || L.act > 3) return cudaErrorInvalidValue;
       J.act = L.act;

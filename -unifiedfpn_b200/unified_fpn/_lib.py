@@ -57,6 +57,8 @@ SIGNATURES = {
     "ufpn_core_set_kernel_config": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int]),
     "ufpn_core_set_schedule": (c_int, [c_void_p, c_int]),
     "ufpn_core_set_schedule_options": (c_int, [c_void_p, c_int, c_int, c_int]),
+    "ufpn_core_set_option": (c_int, [c_void_p, c_char_p, c_int]),
+    "ufpn_core_get_option": (c_int, [c_void_p, c_char_p, POINTER(c_int)]),
     "ufpn_core_trace_next_forward": (c_int, [c_void_p]),
     "ufpn_core_get_neck_trace": (c_int, [c_void_p, POINTER(ctypes.c_ulonglong)]),
     "ufpn_core_get_memory_usage": (c_size_t, [c_void_p]),

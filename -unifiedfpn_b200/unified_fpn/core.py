@@ -327,6 +327,17 @@ class UnifiedFPN:
                                                  int(merge_two_levels)), "set_schedule_options")
         check(lib.ufpn_core_set_fp8_options(self._h, int(fp8_two_pass_p2)), "set_fp8_options")
 
+    def set_option(self, name: str, value: int) -> None:
+        """Named schedule option (``ufpn_core_set_option``): "grouped_topdown" (0/1),
+        "ksplit_p3" / "ksplit_p4" / "ksplit_p5" (1, 2 or 4 units per lateral tile over K in
+        the grouped lateral launch), and the switches of :meth:`set_schedule`."""
+        check(lib.ufpn_core_set_option(self._h, name.encode(), int(value)), f"set_option({name})")
+
+    def get_option(self, name: str) -> int:
+        v = ctypes.c_int(0)
+        check(lib.ufpn_core_get_option(self._h, name.encode(), ctypes.byref(v)), f"get_option({name})")
+        return v.value
+
     def neck_timeline(self, backbone_features) -> dict:
         """Runs one forward with the fused neck kernel's device timeline recorded and
         returns microseconds since the kernel started: when each level's laterals were

@@ -169,6 +169,14 @@ struct FPNKernelConfig {
   // batch-2 and 640x640 batch-16 workloads (one launch, but the P4 3x3 then waits for both
   // merges and the tiles form a single wave that other streams' CTAs cut short).
   bool merge_two_levels = false;
+  // 16-bit split schedule: the grouped lateral launch (P5, P4, P3) also performs the top-down
+  // adds M4 = L4 + up(M5) and M3 = L3 + up(M4) in its epilogues, ordered by device-side level
+  // counters, instead of two merge kernels after it (false: raw laterals, then the merges).
+  bool grouped_topdown = false;
+  // Units per lateral tile over K in the grouped lateral launch, per level (P2..P5; the P2
+  // lateral runs in its own kernel and ignores its entry): 1, 2 or 4.  A long K loop (the P5
+  // lateral's 2048 channels) otherwise holds one SM per tile for its whole weight stream.
+  int lateral_ksplit[4] = {1, 1, 1, 1};
 };
 
 struct FPNWeights {

@@ -235,7 +235,16 @@ struct NeckLevel {
   Conv3x3Tiling lat_tiling, conv_tiling;
   int act = 0;  // the level's 3x3: output activation as TcScales::act, with act_alpha
   float act_alpha = 0.01f;
+  // Split-K lateral of this level (NeckJobSpec::ksplit > 1): fp32 partials
+  // (neck_split_part_bytes) and one arrival counter per lateral tile (neck_lateral_tiles ints,
+  // zero before the first launch; every launch leaves them zero again).
+  float* split_part = nullptr;
+  int* split_sem = nullptr;
 };
+// Lateral tiles of a level's map (one per 128-pixel tile and image).
+int neck_lateral_tiles(int N, int H, int W, Conv3x3Tiling lat_tiling);
+// Bytes of the fp32 partials of a split-K lateral: ksplit x 128 x 256 x 4 per tile.
+size_t neck_split_part_bytes(int N, int H, int W, Conv3x3Tiling lat_tiling, int ksplit);
 struct NeckPlan {
   alignas(64) unsigned char params[6144];  // NeckParams, opaque outside tc_kernels.cu
   DType dtype = DType::BF16;
@@ -253,10 +262,13 @@ cudaError_t plan_neck(NeckPlan& plan, DType dt, int N, const NeckLevel* levels, 
 // jobs before it).  mode 0 = lateral of `level` (coarse = 1: fused top-down add of
 // level+1's merged map), mode 1 = 3x3 of `level`.  A job waits on a level only if that
 // level's lateral runs in the same launch; otherwise its input must be complete before.
+// ksplit (laterals): 1, 2 or 4 units per tile over K, each at least one k-block long; > 1
+// needs the level's split_part / split_sem workspace.
 struct NeckJobSpec {
   int mode;
   int level;
   int coarse;
+  int ksplit = 1;
 };
 cudaError_t plan_neck_jobs(NeckPlan& plan, DType dt, int N, const NeckLevel* levels, void* p6,
                            const NeckJobSpec* specs, int num_specs, int* sched, int* status,

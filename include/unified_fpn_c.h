@@ -110,6 +110,22 @@ int ufpn_core_set_schedule(ufpn_core* core, int fused_neck_kernel);
 int ufpn_core_set_schedule_options(ufpn_core* core, int programmatic_launch, int chain_priority,
                                    int merge_two_levels);
 /* fpn_engine.cu:408-415 (get_memory_usage) */
+/* Named integer options of the schedule (no reference counterpart; the reference's
+ * FPNKernelConfig had fixed fields, types.h:265-293).  Every option keeps the results within
+ * the tolerances; each one's default is the measured faster choice at the R50 800x1216
+ * batch-2 workload, and the autotuner (ufpn_core_autotune) may change them per geometry.
+ *   "grouped_topdown"   0/1  the grouped P5/P4/P3 lateral launch also does the top-down adds
+ *                            of M4 and M3 (device-side level counters) instead of two merge
+ *                            kernels after it (16-bit split schedule)
+ *   "ksplit_p3", "ksplit_p4", "ksplit_p5"
+ *                       1/2/4 units per lateral tile over K in that launch (a last-arriving
+ *                            unit sums the fp32 partials in a fixed order: deterministic)
+ *   "programmatic_launch", "chain_priority", "merge_two_levels", "single_stream",
+ *   "fused_neck_kernel" 0/1  as ufpn_core_set_schedule / ufpn_core_set_schedule_options
+ * Unknown names and values return UFPN_ERR_INVALID_ARG. */
+int ufpn_core_set_option(ufpn_core* core, const char* name, int value);
+int ufpn_core_get_option(const ufpn_core* core, const char* name, int* value);
+
 size_t ufpn_core_get_memory_usage(const ufpn_core* core);
 /* fpn_pytorch.cpp:171-187 (get_performance_breakdown): kernel_times_ms[8], metrics[5] =
  * {forward_ms, GB/s, compute utilisation, peak MiB, kernel launches}. */
@@ -269,14 +285,19 @@ int ufpn_p6_maxpool(int dtype, int layout, const void* p5, void* p6, int N, int 
  * must not create untracked allocations).
  *   inputs: C2..C5, NHWC, dtype BF16/F16; lateral_w[l]: [256][Cin_l] and output_w[l]:
  *   [256][9][256] (ufpn_pack_conv3x3_weights) in the same dtype; biases fp32 [256];
- *   outputs: P2..P5 NHWC; p6 NHWC or NULL; status: optional caller-owned device int that
- *   receives a pipeline-timeout code (NULL = internal).
+ *   outputs: P2..P5 NHWC; p6 NHWC or NULL; levels ordered fine (C2) to coarse (C5).
+ *   status: optional caller-owned device int.  The call zeroes it (stream-ordered) and the
+ *   kernel writes a pipeline-timeout code into it if a bounded wait gives up, so after the
+ *   stream is synchronised it reports this call alone (a caller that wants to watch several
+ *   calls passes a different word to each).  With status = NULL a timeout is not reported
+ *   anywhere the caller can read: the outputs of such a call are undefined.
  * Scratch (merged maps M2..M5 = batch * sum(H_l * W_l) * 512 bytes, plus 512 bytes of
  * counters) lives in a file-scope device array of UFPN_NOALLOC_SCRATCH_BYTES that every
  * GPU loading the library holds until exit; larger problems are rejected with
- * UFPN_ERR_INVALID_ARG.  The first call on a device looks the array's address up
- * (cudaGetSymbolAddress) and should come before any stream capture.  All calls share the
- * array: each clears the counters it needs, and calls that overlap on the GPU race. */
+ * UFPN_ERR_INVALID_ARG.  The first call on a device (and the first after its context was
+ * replaced, e.g. by cudaDeviceReset) looks the array's address up (cudaGetSymbolAddress)
+ * and should come before any stream capture.  All calls share the array: each clears the
+ * counters it needs, and calls that overlap on the GPU race. */
 #define UFPN_NOALLOC_SCRATCH_BYTES (64u << 20)
 int ufpn_neck_forward_noalloc(int dtype, const void* const* inputs,
                               const void* const* lateral_w, const float* const* lateral_b,

@@ -8,7 +8,7 @@ the reference sources are present):
   neck_small.npz   -- digests of the fp32 CPU neck oracle on a small seeded problem
                       (per level: sum, sum of squares and 2048 sampled values).
 
-    make -C oracle && python tests/golden/make_golden.py
+    make -C oracle REF=<reference checkout> && python tests/golden/make_golden.py
 """
 from __future__ import annotations
 

@@ -20,8 +20,9 @@ def _cl(x):
     return x.contiguous(memory_format=torch.channels_last)
 
 
-def _rel(y, ref):
-    return O.rel_err(y.detach().float().cpu(), ref.detach().float())
+def _close(y, ref, kind="grad16", tol=TOL):
+    """Both parity metrics (max-norm ratio <= tol, per-element bound of ``kind``)."""
+    O.check_close(y.detach().float().cpu(), ref.detach().float(), kind, tol=tol)
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
@@ -40,9 +41,9 @@ def test_lateral_conv_backward(cuda_device, dtype, shape):
     wr = wt.float().requires_grad_()
     br = torch.zeros(256, requires_grad=True)
     O.lateral_conv(xr, wr, br).backward(gy.float())
-    assert _rel(gx, xr.grad) < TOL
-    assert _rel(gw, wr.grad) < TOL
-    assert _rel(gb, br.grad) < TOL
+    _close(gx, xr.grad)
+    _close(gw, wr.grad)
+    _close(gb, br.grad)
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
@@ -61,9 +62,9 @@ def test_conv3x3_backward(cuda_device, dtype, shape):
     wr = w3.float().requires_grad_()
     br = torch.zeros(256, requires_grad=True)
     O.conv3x3(xr, wr, br).backward(gy.float())
-    assert _rel(gx, xr.grad) < TOL
-    assert _rel(gw, wr.grad) < TOL
-    assert _rel(gb, br.grad) < TOL
+    _close(gx, xr.grad)
+    _close(gw, wr.grad)
+    _close(gb, br.grad)
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
@@ -81,7 +82,8 @@ def test_upsample_add_backward(cuda_device, dtype, sizes):
     cr = torch.zeros(n, c, hc, wc, requires_grad=True)
     O.bilinear_upsample_t(cr, (h, w)).backward(gy.float())
     ref = cr.grad + base.float()
-    assert _rel(gc, ref) < (1e-5 if dtype == torch.float32 else TOL)
+    _close(gc, ref, "f32" if dtype == torch.float32 else "grad16",
+           1e-5 if dtype == torch.float32 else TOL)
 
 
 def test_p6_backward(cuda_device):
@@ -131,14 +133,14 @@ def test_neck_backward_matches_autograd(cuda_device, dtype, chans, sizes, batch)
     outs_r = O.fpn_neck(feats_r, O.NeckWeights(lw, lb, ow, ob))  # P2..P6
     torch.autograd.backward(outs_r, [gg.float() for gg in grads])
     for o, r in zip(outs, outs_r):  # the forward agrees first
-        assert _rel(o, r) < TOL
+        _close(o, r)
     for f, r in zip(feats, feats_r):
-        assert _rel(f.grad, r.grad) < TOL
+        _close(f.grad, r.grad)
     for l in range(4):
-        assert _rel(neck.lateral_w[l].grad, lw[l].grad) < TOL
-        assert _rel(neck.lateral_b[l].grad, lb[l].grad) < TOL
-        assert _rel(neck.output_w[l].grad, ow[l].grad) < TOL
-        assert _rel(neck.output_b[l].grad, ob[l].grad) < TOL
+        _close(neck.lateral_w[l].grad, lw[l].grad)
+        _close(neck.lateral_b[l].grad, lb[l].grad)
+        _close(neck.output_w[l].grad, ow[l].grad)
+        _close(neck.output_b[l].grad, ob[l].grad)
 
 
 def test_backward_is_deterministic(cuda_device):

@@ -11,8 +11,6 @@ from oracle import fpn_oracle as O
 
 pytestmark = pytest.mark.gpu
 GOLDEN = Path(__file__).resolve().parent / "golden"
-BF16_TOL = O.TOL["bf16"]   # 1e-2 relative to max |ref|
-F32_TOL = O.TOL["f32"]     # 1e-4
 
 
 def _golden_bilinear():
@@ -66,8 +64,7 @@ def test_upsample_add(cuda_device, dtype, layout, sizes):
         cd, ld = _cl(cd), _cl(ld)
     y = U.fpn_upsample_add(cd, ld)
     ref = lat.float() + O.bilinear_upsample_t(coarse.float(), (h, w))
-    tol = F32_TOL if dtype == torch.float32 else BF16_TOL
-    assert O.rel_err(y.cpu(), ref) < tol
+    O.check_close(y.cpu(), ref, dtype)
     if layout == "nhwc":
         assert y.is_contiguous(memory_format=torch.channels_last)
 
@@ -93,8 +90,8 @@ def test_merge_two_levels_bitwise_equals_two_merges(cuda_device, dtype, geom):
     # and against the oracle's two top-down steps
     r4 = l4.cpu().float() + O.bilinear_upsample_t(m5.cpu().float(), (h4, w4))
     r3 = l3.cpu().float() + O.bilinear_upsample_t(r4.to(dtype).float(), (h3, w3))
-    assert O.rel_err(m4.cpu(), r4) < BF16_TOL
-    assert O.rel_err(m3.cpu(), r3) < BF16_TOL
+    O.check_close(m4.cpu(), r4, dtype)
+    O.check_close(m3.cpu(), r3, dtype)
 
 
 def test_reference_abi_upsample_half_and_bf16(cuda_device):
@@ -106,7 +103,7 @@ def test_reference_abi_upsample_half_and_bf16(cuda_device):
         xd = _cl(x.to(dt).to(cuda_device))
         out = _cl(torch.empty(2, 64, 25, 38, dtype=dt, device=cuda_device))
         assert fn(xd.data_ptr(), out.data_ptr(), 2, 64, 13, 19, 25, 38, 0, None, None) == 0
-        assert O.rel_err(out.cpu(), O.bilinear_upsample_t(x.to(dt).float(), (25, 38))) < BF16_TOL
+        O.check_close(out.cpu(), O.bilinear_upsample_t(x.to(dt).float(), (25, 38)), dt)
 
 
 def test_upsample_engine_abi(cuda_device, tmp_path):
@@ -124,7 +121,7 @@ def test_upsample_engine_abi(cuda_device, tmp_path):
     assert "bilinear_upsample_f32" in csv.read_text()
     lib.destroy_upsample_engine(eng)
     ref = O.bilinear_upsample_t(x.cpu().contiguous(), (16, 16))
-    assert O.rel_err(out.cpu(), ref) < F32_TOL
+    O.check_close(out.cpu(), ref, "f32")
 
 
 # ----------------------------------------------------------------------------- P6
@@ -155,7 +152,7 @@ def test_lateral_tc(cuda_device, dtype, shape):
     torch.cuda.synchronize()
     assert U.device_status() == 0
     ref = O.lateral_conv(x.float(), wt.to(dtype).float(), b)
-    assert O.rel_err(y.cpu(), ref) < BF16_TOL
+    O.check_close(y.cpu(), ref, dtype)
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
@@ -172,7 +169,7 @@ def test_lateral_tc_fused_upsample_add(cuda_device, dtype, geom):
     y = U.fpn_lateral_conv(_cl(x.to(cuda_device)), wt.to(cuda_device), b.to(cuda_device),
                            coarse=_cl(coarse.to(cuda_device)))
     ref = O.lateral_conv(x.float(), wt.to(dtype).float(), b) + O.bilinear_upsample_t(coarse.float(), (h, w))
-    assert O.rel_err(y.cpu(), ref) < BF16_TOL
+    O.check_close(y.cpu(), ref, dtype)
     assert U.device_status() == 0
 
 
@@ -203,7 +200,7 @@ def test_lateral_cta_pair(cuda_device, dtype, geom):
     ref = O.lateral_conv(x.float(), wt.to(dtype).float(), b)
     if cg:
         ref = ref + O.bilinear_upsample_t(coarse.float(), (h, w))
-    assert O.rel_err(y.cpu(), ref) < BF16_TOL
+    O.check_close(y.cpu(), ref, dtype)
     ulp = ref.abs() * (2.0 ** -8 if dtype == torch.bfloat16 else 2.0 ** -11)  # half an ulp, at most
     assert ((y.cpu().float() - ref).abs() <= 2.01 * ulp + 1e-5 * ref.abs().max()).all()
 
@@ -229,7 +226,7 @@ def test_lateral_fp32_config1(cuda_device):
     c3, p4, w, b = O.config1_inputs(seed=0)
     y = U.fpn_lateral_conv(c3.to(cuda_device), w.to(cuda_device), b.to(cuda_device), coarse=p4.to(cuda_device))
     ref = O.fused_lateral_upsample(c3, p4, w, b)
-    assert O.rel_err(y.cpu(), ref) < F32_TOL
+    O.check_close(y.cpu(), ref, "f32")
 
 
 # ----------------------------------------------------------------------------- 3x3 (tcgen05)
@@ -242,7 +239,7 @@ def test_conv3x3_tc_tilings(cuda_device, tile_w):
     b = torch.rand(256, generator=g) * 0.2 - 0.1
     y = U.fpn_conv3x3(_cl(x.to(cuda_device)), w.to(cuda_device), b.to(cuda_device), tile_w=tile_w)
     ref = O.conv3x3(x.float(), w.to(torch.bfloat16).float(), b)
-    assert O.rel_err(y.cpu(), ref) < BF16_TOL
+    O.check_close(y.cpu(), ref, "bf16")
     assert U.device_status() == 0
 
 
@@ -257,7 +254,7 @@ def test_conv3x3_tc_with_p6(cuda_device, dtype, shape):
     b = torch.rand(256, generator=g) * 0.2 - 0.1
     y, p6 = U.fpn_conv3x3(_cl(x.to(cuda_device)), w.to(cuda_device), b.to(cuda_device), p6=True)
     ref = O.conv3x3(x.float(), w.to(dtype).float(), b)
-    assert O.rel_err(y.cpu(), ref) < BF16_TOL
+    O.check_close(y.cpu(), ref, dtype)
     assert torch.equal(p6.cpu(), y.cpu()[:, :, ::2, ::2])
 
 
@@ -284,7 +281,7 @@ def test_conv3x3_cta_pair_equals_single(cuda_device, dtype, shape):
     assert torch.equal(y1, y2) and torch.equal(p1, p2)
     if n * h * w_ <= 4096:
         ref = O.conv3x3(x.float(), w.to(dtype).float(), b)
-        assert O.rel_err(y2.cpu(), ref) < BF16_TOL
+        O.check_close(y2.cpu(), ref, dtype)
 
 
 def test_conv3x3_fp32(cuda_device):
@@ -294,7 +291,7 @@ def test_conv3x3_fp32(cuda_device):
     w = torch.randn(256, 256, 3, 3, generator=g) * (2.0 / 2304) ** 0.5
     b = torch.rand(256, generator=g) * 0.2 - 0.1
     y = U.fpn_conv3x3(x.to(cuda_device), w.to(cuda_device), b.to(cuda_device))
-    assert O.rel_err(y.cpu(), O.conv3x3(x, w, b)) < F32_TOL
+    O.check_close(y.cpu(), O.conv3x3(x, w, b), "f32")
 
 
 def test_layout_convert_roundtrip(cuda_device):
@@ -328,7 +325,7 @@ def test_conv3x3_activation_epilogue(cuda_device, dtype, tile_w, act, alpha):
     torch.cuda.synchronize()
     assert U.device_status() == 0
     ref = O.activation(O.conv3x3(x.float(), w.to(dtype).float(), b), act, alpha)
-    assert O.rel_err(y.float().cpu(), ref) < (F32_TOL if dtype == torch.float32 else BF16_TOL)
+    O.check_close(y.float().cpu(), ref, dtype)
     assert torch.equal(p6.cpu(), y.cpu()[:, :, ::2, ::2])
     if act == "relu":
         assert y.min().item() >= 0

@@ -217,3 +217,31 @@ def test_oracle_bilinear_ramp_closed_form():
     assert np.allclose(np.diff(out[0, 0, 8:24, 8:24], axis=1), 0.5)
     assert np.allclose(np.diff(out[0, 0, 8:24, 8:24], axis=0), 8.0)
     assert np.all(out[0, 1:] == out[0, :1])  # every channel the same
+
+
+def test_elem_err_catches_what_the_max_norm_ratio_misses():
+    """Two mistakes planted in a 3x3 output (on the CPU): a tile-seam row computed without the
+    halo row below it, which both metrics flag, and a 20 % error confined to one 8 x 16 tile
+    of one low-magnitude output channel, which stays under the max-norm ratio's 1e-2 of the
+    level's largest value but breaks the per-element bound."""
+    torch.manual_seed(0)
+    m = torch.randn(1, 256, 48, 40)
+    w = torch.randn(256, 256, 3, 3) * (2.0 / 2304) ** 0.5
+    w[7] *= 0.05  # a channel with small outputs
+    b = torch.zeros(256)
+    ref = O.conv3x3(m, w, b)
+    assert O.elem_err(ref, ref, "bf16") == 0.0
+    seam = ref.clone()
+    cut = m.clone()
+    cut[:, :, 16:] = 0  # the rows below the first 16-row tile missing from its halo
+    seam[:, :, 15] = O.conv3x3(cut, w, b)[:, :, 15]
+    assert O.rel_err(seam, ref) > O.TOL["bf16"] and O.elem_err(seam, ref, "bf16") > 1.0
+    local = ref.clone()
+    local[:, 7, 16:32, 8:16] *= 1.2
+    assert O.rel_err(local, ref) < O.TOL["bf16"]       # the max-norm ratio lets it through
+    assert O.elem_err(local, ref, "bf16") > 1.0        # the per-element bound does not
+    with pytest.raises(AssertionError):
+        O.check_close(local, ref, "bf16")
+    # bf16-sized rounding noise everywhere passes both
+    noisy = ref * (1 + 2.0 ** -9 * torch.randn_like(ref).clamp(-1, 1))
+    O.check_close(noisy, ref, "bf16")
