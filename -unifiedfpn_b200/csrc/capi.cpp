@@ -105,6 +105,23 @@ const char* ufpn_last_error(void) { return g_last_error.c_str(); }
 
 int ufpn_version(void) { return 100; }
 
+int ufpn_set_peaks(double tensor_tflops, double fp32_tflops, double hbm_gbs) {
+  if (!(tensor_tflops >= 0) || !(fp32_tflops >= 0) || !(hbm_gbs >= 0))
+    return fail(UFPN_ERR_INVALID_ARG, "peaks must be >= 0 (0 keeps the current value)");
+  ufpn::set_device_peaks(tensor_tflops * 1e12, fp32_tflops * 1e12, hbm_gbs * 1e9);
+  return UFPN_OK;
+}
+
+int ufpn_get_peaks(double* out3) {
+  if (!out3) return fail(UFPN_ERR_INVALID_ARG, "NULL");
+  double pk[3];
+  ufpn::get_device_peaks(pk);
+  out3[0] = pk[0] / 1e12;
+  out3[1] = pk[1] / 1e12;
+  out3[2] = pk[2] / 1e9;
+  return UFPN_OK;
+}
+
 int ufpn_device_status(int reset, int* status_out) {
   int* w = device_status_word();
   if (!w) return fail(UFPN_ERR_CUDA, "could not allocate the device status word");
@@ -293,10 +310,13 @@ struct OptionField {
 };
 bool valid_bool(int v) { return v == 0 || v == 1; }
 bool valid_ksplit(int v) { return v == 1 || v == 2 || v == 4; }
+bool valid_stall(int v) { return v >= 0 && v <= 1000000; }  // at most 1 s
 const OptionField kOptions[] = {
     {"ksplit_p3", [](FPNKernelConfig& c) { return &c.lateral_ksplit[1]; }, valid_ksplit},
     {"ksplit_p4", [](FPNKernelConfig& c) { return &c.lateral_ksplit[2]; }, valid_ksplit},
     {"ksplit_p5", [](FPNKernelConfig& c) { return &c.lateral_ksplit[3]; }, valid_ksplit},
+    {"test_stall_dependency_us", [](FPNKernelConfig& c) { return &c.test_stall_dependency_us; },
+     valid_stall},
 };
 // Boolean options (stored as bool in FPNKernelConfig).
 struct BoolOption {
@@ -349,6 +369,12 @@ int ufpn_core_get_option(const ufpn_core* core, const char* name, int* value) {
       return UFPN_OK;
     }
   return fail(UFPN_ERR_INVALID_ARG, std::string("unknown option ") + name);
+}
+
+int ufpn_core_graph_stats(const ufpn_core* core, long long* out4) {
+  if (!core || !out4) return fail(UFPN_ERR_INVALID_ARG, "NULL argument");
+  core->core.graph_stats(out4);
+  return UFPN_OK;
 }
 
 size_t ufpn_core_get_memory_usage(const ufpn_core* core) {

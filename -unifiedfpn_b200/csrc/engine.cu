@@ -16,6 +16,7 @@
 // per (pointer set) into a CUDA graph on a private stream and replayed with a
 // single cudaGraphLaunch on the caller's stream.
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <fstream>
@@ -77,6 +78,25 @@ Conv3x3Tiling tiling_from_code(int tw) {
 }
 
 }  // namespace
+
+namespace ufpn {
+// Peaks the profiled forward's utilisation figures are reported against (set_device_peaks):
+// dense 16-bit tensor FLOP/s (e4m3 counts twice that), fp32 CUDA-core FLOP/s, HBM bytes/s.
+// Nominal B200 figures until a caller sets measured ones.
+namespace {
+std::atomic<double> g_peak_tensor{2.25e15}, g_peak_fp32{8.0e13}, g_peak_hbm{8.0e12};
+}
+void set_device_peaks(double tensor_flops, double fp32_flops, double hbm_bytes) {
+  if (tensor_flops > 0) g_peak_tensor.store(tensor_flops);
+  if (fp32_flops > 0) g_peak_fp32.store(fp32_flops);
+  if (hbm_bytes > 0) g_peak_hbm.store(hbm_bytes);
+}
+void get_device_peaks(double* out3) {
+  out3[0] = g_peak_tensor.load();
+  out3[1] = g_peak_fp32.load();
+  out3[2] = g_peak_hbm.load();
+}
+}  // namespace ufpn
 
 struct UnifiedFPNCore::Impl {
   int device = 0;
@@ -152,6 +172,15 @@ struct UnifiedFPNCore::Impl {
     int launches;
   };
   std::vector<GraphEntry> graphs;
+  // Pointer sets seen once and not captured (capture happens on a set's second use).
+  struct SeenKey {
+    const void* in[4];
+    const float* scale[4];
+    void* out[4];
+    void* p6;
+  };
+  std::vector<SeenKey> seen_once;
+  long long stat_captures = 0, stat_replays = 0, stat_direct = 0;
   std::map<std::string, std::pair<int, float>> tuning_db;  // key -> (tile_w, ms)
 
   ~Impl() { release_all(); }
@@ -159,6 +188,7 @@ struct UnifiedFPNCore::Impl {
   void release_graphs() {
     for (auto& g : graphs) cudaGraphExecDestroy(g.exec);
     graphs.clear();
+    seen_once.clear();
   }
   void free_workspace() {
     for (int l = 0; l < 4; ++l) {
@@ -278,6 +308,13 @@ struct UnifiedFPNCore::Impl {
       if (e) cudaEventDestroy(e);
   }
 
+  // Stage-timing event of the profiled forward.  That forward is captured into a graph, and
+  // only an external event record (not the dependency-only node a plain record becomes
+  // during capture) can be timed after the replay.
+  void prof_record(int k, cudaStream_t st) {
+    cudaEventRecordWithFlags(prof[k], st, cudaEventRecordExternal);
+  }
+
   bool tensor_core_path() const { return dtype != DType::F32 && cfg.use_tensor_cores; }
   int act() const { return static_cast<int>(cfg.activation); }
   ufpn::TcScales act_scales() const {
@@ -361,14 +398,14 @@ struct UnifiedFPNCore::Impl {
     };
     if (!tensor_core_path()) {
       // fp32 CUDA-core path, NCHW, all on one stream.
-      if (prof_events) cudaEventRecord(prof[0], main);
+      if (prof_events) prof_record(0, main);
       for (int l = 3; l >= 0; --l) {
         const float* coarse = l < 3 ? static_cast<const float*>(merged[l + 1]) : nullptr;
         ok(ufpn::launch_fp32_lateral(static_cast<const float*>(in[l]), lat_w32[l], lat_b[l],
                                      coarse, static_cast<float*>(merged[l]), batch, cin[l], cout,
                                      H[l], W[l], l < 3 ? H[l + 1] : 1, l < 3 ? W[l + 1] : 1, main),
            "fp32 lateral");
-        if (prof_events) cudaEventRecord(prof[1 + 2 * (3 - l)], main);
+        if (prof_events) prof_record(1 + 2 * (3 - l), main);
         ok(ufpn::launch_fp32_conv3x3(static_cast<const float*>(merged[l]), out_w32[l], out_b[l],
                                      static_cast<float*>(out[l]), batch, cout, cout, H[l], W[l],
                                      main, act(), cfg.activation_alpha),
@@ -376,7 +413,7 @@ struct UnifiedFPNCore::Impl {
         if (l == 3 && p6)
           ok(ufpn::launch_p6(DType::F32, out[3], p6, batch, cout, H[3], W[3], Layout::NCHW, main),
              "p6");
-        if (prof_events) cudaEventRecord(prof[2 + 2 * (3 - l)], main);
+        if (prof_events) prof_record(2 + 2 * (3 - l), main);
       }
       return launches;
     }
@@ -390,7 +427,7 @@ struct UnifiedFPNCore::Impl {
       o[l] = nchw ? nhwc_out[l] : out[l];
       x[l] = in[l];
     }
-    if (prof_events) cudaEventRecord(prof[0], main);
+    if (prof_events) prof_record(0, main);
     if (nchw) {
       for (int l = 3; l >= 0; --l) {
         ok(ufpn::launch_transpose(dtype, in[l], nhwc_in[l], batch, cin[l], H[l] * W[l], true,
@@ -421,6 +458,10 @@ struct UnifiedFPNCore::Impl {
       check(ufpn::plan_neck(plan, dtype, batch, lv, o6, d_sched, d_status, 0,
                             trace_next ? d_trace : nullptr),
             "plan neck");
+      if (cfg.test_stall_dependency_us > 0)
+        check(ufpn::neck_plan_stall_dependency(
+                  plan, 0, static_cast<unsigned long long>(cfg.test_stall_dependency_us) * 1000ull),
+              "stall self-test");
       ok(ufpn::launch_neck(plan, main), "neck launch");
       if (nchw) {
         for (int l = 0; l < 4; ++l)
@@ -503,41 +544,41 @@ struct UnifiedFPNCore::Impl {
                                trace_next ? d_trace : nullptr),
           "plan grouped laterals");
     ok(ufpn::launch_neck(gplan, main, nchw ? chain : chain_first), "grouped laterals launch");
-    if (prof_events) cudaEventRecord(prof[1], main);
+    if (prof_events) prof_record(1, main);
     conv_level(3);
-    if (prof_events) cudaEventRecord(prof[2], main);
+    if (prof_events) prof_record(2, main);
     if (td) {
       // M4 and M3 are complete: no merge stages (their profile slots stay empty).
-      if (prof_events) cudaEventRecord(prof[3], main);
+      if (prof_events) prof_record(3, main);
       conv_level(2);
       if (prof_events) {
-        cudaEventRecord(prof[4], main);
-        cudaEventRecord(prof[5], main);
+        prof_record(4, main);
+        prof_record(5, main);
       }
       conv_level(1);
-      if (prof_events) cudaEventRecord(prof[6], main);
+      if (prof_events) prof_record(6, main);
     } else if (two_level) {
       ok(ufpn::launch_merge_two_levels(dtype, merged[3], lat4_raw, merged[2], merged[1],
                                        merged[1], batch, H[3], W[3], H[2], W[2], H[1], W[1],
                                        main, nullptr, nullptr, nullptr, chain),
          "merge P4 and P3");
-      if (prof_events) cudaEventRecord(prof[3], main);
+      if (prof_events) prof_record(3, main);
       conv_level(2);
       if (prof_events) {
-        cudaEventRecord(prof[4], main);
-        cudaEventRecord(prof[5], main);  // (no separate P3 merge)
+        prof_record(4, main);
+        prof_record(5, main);  // (no separate P3 merge)
       }
       conv_level(1);
-      if (prof_events) cudaEventRecord(prof[6], main);
+      if (prof_events) prof_record(6, main);
     } else {
       for (int l = 2; l >= 1; --l) {
         ok(ufpn::launch_upsample_add(dtype, merged[l + 1], merged[l], merged[l], batch, cout,
                                      H[l + 1], W[l + 1], H[l], W[l], 0, Layout::NHWC, main,
                                      nullptr, nullptr, chain),
            "merge");
-        if (prof_events) cudaEventRecord(prof[3 + 2 * (2 - l)], main);
+        if (prof_events) prof_record(3 + 2 * (2 - l), main);
         conv_level(l);
-        if (prof_events) cudaEventRecord(prof[4 + 2 * (2 - l)], main);
+        if (prof_events) prof_record(4 + 2 * (2 - l), main);
       }
     }
     TcPlan lat2;
@@ -547,9 +588,9 @@ struct UnifiedFPNCore::Impl {
           "plan lateral");
     ufpn::tc_attach_wb_table(lat2, wb_table);
     ok(ufpn::launch_tc(lat2, main, chain), "lateral launch");
-    if (prof_events) cudaEventRecord(prof[7], main);
+    if (prof_events) prof_record(7, main);
     conv_level(0);
-    if (prof_events) cudaEventRecord(prof[8], main);
+    if (prof_events) prof_record(8, main);
     if (!one_stream) join_conv_streams(main);
     if (nchw) {
       for (int l = 0; l < 4; ++l)
@@ -608,7 +649,7 @@ struct UnifiedFPNCore::Impl {
       return o;
     };
     const bool two_level = lat4_raw != nullptr && cfg.merge_two_levels;
-    if (prof_events) cudaEventRecord(prof[0], main);
+    if (prof_events) prof_record(0, main);
     check(cudaMemsetAsync(fp8_amax, 0, 4 * static_cast<size_t>(batch) * sizeof(unsigned), main),
           "memset");
     if (!one_stream) {
@@ -685,9 +726,9 @@ struct UnifiedFPNCore::Impl {
       lateral(2 - i, nullptr, nullptr, st, one_stream);
       if (!one_stream) check(cudaEventRecord(ev_lat_done[i], st), "event");
     }
-    if (prof_events) cudaEventRecord(prof[1], main);
+    if (prof_events) prof_record(1, main);
     conv_level(3);
-    if (prof_events) cudaEventRecord(prof[2], main);
+    if (prof_events) prof_record(2, main);
     // M3 also gets its copy pre-divided by the P2 lateral's per-channel scale, which the P2
     // lateral adds through its tensor-core top-down k-block.
     ufpn::MergeScaledCopy m3s;
@@ -702,14 +743,14 @@ struct UnifiedFPNCore::Impl {
                                        main, fp8_amax + 2 * batch, fp8_amax + batch, &m3s,
                                        opts(pdl)),
          "merge P4 and P3");
-      if (prof_events) cudaEventRecord(prof[3], main);
+      if (prof_events) prof_record(3, main);
       conv_level(2);
       if (prof_events) {
-        cudaEventRecord(prof[4], main);
-        cudaEventRecord(prof[5], main);  // (no separate P3 merge)
+        prof_record(4, main);
+        prof_record(5, main);  // (no separate P3 merge)
       }
       conv_level(1);
-      if (prof_events) cudaEventRecord(prof[6], main);
+      if (prof_events) prof_record(6, main);
     } else {
       for (int l = 2; l >= 1; --l) {
         if (!one_stream) check(cudaStreamWaitEvent(main, ev_lat_done[2 - l], 0), "event");
@@ -717,9 +758,9 @@ struct UnifiedFPNCore::Impl {
                                      cout, H[l + 1], W[l + 1], H[l], W[l], 0, Layout::NHWC, main,
                                      fp8_amax + l * batch, l == 1 ? &m3s : nullptr, opts(pdl)),
            "merge");
-        if (prof_events) cudaEventRecord(prof[3 + 2 * (2 - l)], main);
+        if (prof_events) prof_record(3 + 2 * (2 - l), main);
         conv_level(l);
-        if (prof_events) cudaEventRecord(prof[4 + 2 * (2 - l)], main);
+        if (prof_events) prof_record(4 + 2 * (2 - l), main);
       }
     }
     if (cfg.fp8_two_pass_p2) {
@@ -729,9 +770,9 @@ struct UnifiedFPNCore::Impl {
     } else {
       lateral(0, m3_scaled, fp8_amax, main, true);
     }
-    if (prof_events) cudaEventRecord(prof[7], main);
+    if (prof_events) prof_record(7, main);
     conv_level(0, !cfg.fp8_two_pass_p2);
-    if (prof_events) cudaEventRecord(prof[8], main);
+    if (prof_events) prof_record(8, main);
     if (!one_stream) join_conv_streams(main);
     return launches;
   }
@@ -975,20 +1016,42 @@ void UnifiedFPNCore::forward_raw_scaled(const void* const* in, const float* cons
   m.ensure_weight_packing();
   m.ensure_split_workspace();
   if (m.profiling) {
-    const int n = m.enqueue(in, out, p6, stream, true);
-    m.check(cudaEventRecord(m.prof[9], stream), "event");
-    m.check(cudaEventSynchronize(m.prof[9]), "event");
+    // The serialised schedule with an event between stages, captured and replayed as one
+    // graph: the host's planning (tensor-map encoding) happens at capture, so the stage
+    // times are device time only.
+    cudaGraph_t graph = nullptr;
+    m.check(cudaStreamBeginCapture(m.capture, cudaStreamCaptureModeThreadLocal), "capture");
+    int n = 0;
+    try {
+      n = m.enqueue(in, out, p6, m.capture, true);
+    } catch (...) {
+      cudaStreamEndCapture(m.capture, &graph);
+      if (graph) cudaGraphDestroy(graph);
+      throw;
+    }
+    m.check(cudaStreamEndCapture(m.capture, &graph), "capture");
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    m.check(ie, "cudaGraphInstantiate");
+    const cudaError_t le = cudaGraphLaunch(exec, stream);
+    if (le == cudaSuccess) cudaEventRecord(m.prof[9], stream);
+    const cudaError_t se = le == cudaSuccess ? cudaEventSynchronize(m.prof[9]) : le;
+    cudaGraphExecDestroy(exec);
+    m.check(se, "profiled forward");
     float total = 0.f;
     for (int k = 0; k < 8; ++k) {
       float t = 0.f;
-      cudaEventElapsedTime(&t, m.prof[k], m.prof[k + 1]);
+      m.check(cudaEventElapsedTime(&t, m.prof[k], m.prof[k + 1]), "stage time");
       m.metrics.kernel_times_ms[k] = t;
     }
-    cudaEventElapsedTime(&total, m.prof[0], m.prof[9]);
+    m.check(cudaEventElapsedTime(&total, m.prof[0], m.prof[9]), "forward time");
     m.metrics.forward_time_ms = total;
     m.metrics.memory_bandwidth_gb_s =
         total > 0 ? static_cast<float>(m.compulsory_bytes() / (total * 1e-3) / 1e9) : 0.f;
-    const double peak = m.tensor_core_path() ? 2.25e15 : 8.0e13;  // nominal dense peaks
+    double pk[3];
+    ufpn::get_device_peaks(pk);
+    const double peak = !m.tensor_core_path() ? pk[1] : (m.dtype == DType::E4M3 ? 2.0 * pk[0] : pk[0]);
     m.metrics.compute_utilization =
         total > 0 ? static_cast<float>(m.flops() / (total * 1e-3) / peak) : 0.f;
     m.metrics.num_kernel_launches = n;
@@ -1017,8 +1080,37 @@ void UnifiedFPNCore::forward_raw_scaled(const void* const* in, const float* cons
       if (hit) {
         m.check(cudaGraphLaunch(e.exec, stream), "cudaGraphLaunch");
         m.metrics.num_kernel_launches = e.launches;
+        ++m.stat_replays;
         return;
       }
+    }
+    // A pointer set is captured on its second use; the first runs as direct launches (a
+    // caller that allocates new outputs every call pays launch latency, not a capture and
+    // instantiation per call, and does not evict the graphs of sets that do repeat).
+    bool seen = false;
+    for (size_t i = 0; i < m.seen_once.size() && !seen; ++i) {
+      const auto& k = m.seen_once[i];
+      bool hit = k.p6 == p6;
+      for (int l = 0; l < 4 && hit; ++l)
+        hit = k.in[l] == in[l] && k.out[l] == out[l] && k.scale[l] == m.in_scale[l];
+      if (hit) {
+        seen = true;
+        m.seen_once.erase(m.seen_once.begin() + static_cast<long>(i));
+      }
+    }
+    if (!seen) {
+      Impl::SeenKey k;
+      for (int l = 0; l < 4; ++l) {
+        k.in[l] = in[l];
+        k.out[l] = out[l];
+        k.scale[l] = m.in_scale[l];
+      }
+      k.p6 = p6;
+      if (m.seen_once.size() >= 16) m.seen_once.erase(m.seen_once.begin());
+      m.seen_once.push_back(k);
+      m.metrics.num_kernel_launches = m.enqueue(in, out, p6, stream, false);
+      ++m.stat_direct;
+      return;
     }
     // Capture on the private stream (capturing the legacy default stream is not
     // allowed), ordered after the caller's prior work by the graph launch itself.
@@ -1053,6 +1145,7 @@ void UnifiedFPNCore::forward_raw_scaled(const void* const* in, const float* cons
     e.exec = exec;
     e.launches = n;
     m.graphs.push_back(e);
+    ++m.stat_captures;
     m.check(cudaGraphLaunch(exec, stream), "cudaGraphLaunch");
     m.metrics.num_kernel_launches = n;
     return;
@@ -1102,6 +1195,13 @@ size_t UnifiedFPNCore::get_memory_usage() const {
 }
 
 void UnifiedFPNCore::set_profiling(bool enable) { impl_->profiling = enable; }
+
+void UnifiedFPNCore::graph_stats(long long* out4) const {
+  out4[0] = impl_->stat_captures;
+  out4[1] = impl_->stat_replays;
+  out4[2] = impl_->stat_direct;
+  out4[3] = static_cast<long long>(impl_->graphs.size());
+}
 
 void UnifiedFPNCore::trace_next_forward() { impl_->trace_next = true; }
 

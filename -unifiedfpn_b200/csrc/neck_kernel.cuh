@@ -89,6 +89,9 @@ struct NeckParams {
   int lat_tiles[4];  // lateral tiles per level (completion targets)
   int* sched;   // [0] tile counter, [1 + l] completed lateral tiles of level l, [7] exit counter
   int* status;  // device status word
+  // Limit of the level-dependency waits in ns (0: kWaitTimeoutNs).  Shortened only by the
+  // wait-timeout self-test (neck_plan_stall_dependency).
+  unsigned long long dep_wait_ns;
   // Optional timeline (globaltimer ns): [0] first CTA start (min), [1 + l] time level l's
   // laterals completed, [5] last CTA end (max), [6] first conv2 tile MMA start (min).
   unsigned long long* trace;
@@ -129,7 +132,8 @@ __device__ __forceinline__ bool epi_vote_all(bool v) {
 
 // Bounded wait until *counter >= target (acquire).  Returns false on timeout/abort.
 __device__ __forceinline__ bool wait_counter(const int* counter, int target,
-                                             volatile int* abort_flag, int* status, int code) {
+                                             volatile int* abort_flag, int* status, int code,
+                                             unsigned long long limit_ns = kWaitTimeoutNs) {
   if (ld_acquire_gpu(counter) >= target) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
@@ -139,7 +143,7 @@ __device__ __forceinline__ bool wait_counter(const int* counter, int target,
       if (ld_acquire_gpu(counter) >= target) return true;
     }
     if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       *abort_flag = 1;
       if (status) atomicCAS(status, 0, code);
       return false;
@@ -296,7 +300,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         neck_unit_kb(jb, part, kb0, kb1);
         if (jb.mode == 1 && jb.dep_level >= 0 && !(ready_level_mask & (1 << jb.dep_level))) {
           if (!wait_counter(&sched[1 + jb.dep_level], jb.dep_count, abort_flag, P.status,
-                            kDevTimeoutDependency)) {
+                            kDevTimeoutDependency,
+                            P.dep_wait_ns ? P.dep_wait_ns : kWaitTimeoutNs)) {
             ok = false;
             break;
           }

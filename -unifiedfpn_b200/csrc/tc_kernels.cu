@@ -657,6 +657,20 @@ cudaError_t plan_neck_jobs(NeckPlan& plan, DType dt, int N, const NeckLevel* lv,
   return cudaSuccess;
 }
 
+cudaError_t neck_plan_stall_dependency(NeckPlan& plan, int level, unsigned long long wait_ns) {
+  NeckParams* P = reinterpret_cast<NeckParams*>(plan.params);
+  if (wait_ns == 0 || level < 0 || level > 3) return cudaErrorInvalidValue;
+  for (int j = 0; j < P->num_jobs; ++j) {
+    NeckJob& J = P->jobs[j];
+    if (J.mode == 1 && J.level == level && J.dep_level == level) {
+      J.dep_count += 1;  // one more lateral tile than the level has: never reached
+      P->dep_wait_ns = wait_ns;
+      return cudaSuccess;
+    }
+  }
+  return cudaErrorInvalidValue;  // no 3x3 of that level waits on its lateral in this plan
+}
+
 cudaError_t plan_neck(NeckPlan& plan, DType dt, int N, const NeckLevel* lv, void* p6,
                       int* sched, int* status, int max_ctas, unsigned long long* trace) {
   // Dispatch order: each job only depends on jobs before it.  All laterals go first:

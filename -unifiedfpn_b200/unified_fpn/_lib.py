@@ -21,6 +21,13 @@ ERR_DEVICE_TIMEOUT = 4
 ERR_STATE = 5
 ERR_ALIGNMENT = 6
 
+# device status words (the role whose bounded wait gave up first)
+DEV_TIMEOUT_PRODUCER = 0x101
+DEV_TIMEOUT_MMA = 0x102
+DEV_TIMEOUT_EPILOGUE = 0x103
+DEV_TIMEOUT_DRAIN = 0x104
+DEV_TIMEOUT_DEPENDENCY = 0x105
+
 DTYPE_F32 = 0
 DTYPE_F16 = 1
 DTYPE_BF16 = 2
@@ -58,6 +65,9 @@ SIGNATURES = {
     "ufpn_core_set_schedule": (c_int, [c_void_p, c_int]),
     "ufpn_core_set_schedule_options": (c_int, [c_void_p, c_int, c_int, c_int]),
     "ufpn_core_set_option": (c_int, [c_void_p, c_char_p, c_int]),
+    "ufpn_set_peaks": (c_int, [ctypes.c_double, ctypes.c_double, ctypes.c_double]),
+    "ufpn_core_graph_stats": (c_int, [c_void_p, POINTER(c_longlong)]),
+    "ufpn_get_peaks": (c_int, [POINTER(ctypes.c_double)]),
     "ufpn_core_get_option": (c_int, [c_void_p, c_char_p, POINTER(c_int)]),
     "ufpn_core_trace_next_forward": (c_int, [c_void_p]),
     "ufpn_core_get_neck_trace": (c_int, [c_void_p, POINTER(ctypes.c_ulonglong)]),

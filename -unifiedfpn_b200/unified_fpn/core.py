@@ -273,8 +273,12 @@ class UnifiedFPN:
             px = t.shape[0] * t.shape[2] * t.shape[3]
             nbytes += px * (t.shape[1] * esz + 256 * osz)
             flops += 2.0 * px * 256 * (t.shape[1] + 9 * 256)
-        # nominal dense peaks: e4m3 4.5, bf16/fp16 2.25 PFLOP/s; fp32 CUDA cores 80 TFLOP/s
-        peak = {torch.float32: 8.0e13, E4M3: 4.5e15}.get(feats[0].dtype, 2.25e15)
+        # against the peaks set for the library (measured ones when a peaks file is present,
+        # else nominal B200 figures; see unified_fpn.set_peaks); e4m3 counts twice the 16-bit rate
+        from .helpers import get_peaks
+        pk = get_peaks()
+        peak = {torch.float32: pk["fp32_tflops"] * 1e12,
+                E4M3: 2.0 * pk["tensor_tflops"] * 1e12}.get(feats[0].dtype, pk["tensor_tflops"] * 1e12)
         return ms, nbytes / (ms * 1e-3) / 1e9, flops / (ms * 1e-3) / peak
 
     def get_performance_breakdown(self, backbone_features=None, input_scales=None):
@@ -350,6 +354,13 @@ class UnifiedFPN:
         us = lambda v: (v - t0) / 1e3 if v else None  # noqa: E731
         return {"lat_P5_done": us(tr[4]), "lat_P4_done": us(tr[3]), "lat_P3_done": us(tr[2]),
                 "lat_P2_done": us(tr[1]), "conv_P2_first_tile": us(tr[6]), "end": us(tr[5])}
+
+    def graph_stats(self) -> dict:
+        """Graph cache counters: pointer sets captured (on their second use), graph replays,
+        forwards launched directly (a pointer set's first use) and graphs cached now."""
+        v = (ctypes.c_longlong * 4)()
+        check(lib.ufpn_core_graph_stats(self._h, v), "graph_stats")
+        return {"captures": v[0], "replays": v[1], "direct": v[2], "cached": v[3]}
 
     def get_memory_usage(self) -> int:
         return int(lib.ufpn_core_get_memory_usage(self._h))

@@ -14,6 +14,10 @@ Prints ONE JSON line (rank 0).  Keys beyond the base contract:
   roofline    the dominant kernel (P2 3x3 implicit GEMM) timed live with CUDA events
   cpu_baseline  the CPU oracle neck (fp32 torch CPU, all host threads) on a bounded sample
   clocks      nvidia-smi samples taken during the timed window
+  extra       (N = 1) the other configurations' per-GPU shards timed after the headline:
+              e4m3 R50 640x640 16 images, bf16 R50 1024x1024 8 images, bf16 Swin 1333x800
+              8 images, and the fp32 single-level lateral + top-down op
+  per_rank_ms_per_step  (N > 1) every rank's step time
 
 --train times the neck's training step instead (its own JSON line, metric METRIC_TRAIN): the
 forward of unified_fpn.FPNNeck (fp32 master weights, 16-bit kernels) and the backward to every
@@ -90,6 +94,140 @@ def job_throughput(ms_local, images_local, world, device=None):
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     dist.all_reduce(n, op=dist.ReduceOp.SUM)
     return float(t.item()), int(round(n.item()))
+
+
+def per_rank_ms(ms_local, world, device=None):
+    """Every rank's step time (ms), gathered outside the timed window (N > 1: names the
+    straggler behind the max-over-ranks figure)."""
+    if world <= 1:
+        return None
+    import torch.distributed as dist
+    t = torch.tensor([float(ms_local)], dtype=torch.float64, device=device)
+    out = [torch.zeros_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [round(float(x.item()), 5) for x in out]
+
+
+def time_steps(fn, steps, warmup=3, stream=None):
+    """ms per call of fn() (CUDA events on the current stream, after warm-up)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def extra_workloads(dev, peaks):
+    """The other configurations' per-GPU shards, timed in the same run (not the headline):
+    each the whole neck through UnifiedFPN on device-resident inputs rotating over 2 sets,
+    with its own neck roofline (slower of FLOPs at the sustained tensor peak and compulsory
+    bytes at HBM peak); the fp32 single-level op with its GB/s and FFMA fraction."""
+    import unified_fpn as U
+    res = {}
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7)
+
+    def neck(name, chans, sizes, batch, dtype, steps):
+        fp8 = dtype == torch.float8_e4m3fn
+        sets, scs = [], []
+        for _ in range(2):
+            if fp8:
+                qs = [U.quantize_fp8(torch.randn(batch, c, h, w, device=dev, generator=gen).contiguous(
+                    memory_format=torch.channels_last)) for c, (h, w) in zip(chans, sizes)]
+                sets.append([q for q, _ in qs])
+                scs.append(torch.cat([sc for _, sc in qs]))
+            else:
+                sets.append([torch.randn(batch, c, h, w, device=dev, generator=gen).to(dtype)
+                             .contiguous(memory_format=torch.channels_last) for c, (h, w) in zip(chans, sizes)])
+                scs.append(None)
+        fpn = U.UnifiedFPN(device=dev)
+        outs = [fpn(sets[i], return_p6=True, input_scales=scs[i]) for i in range(2)]
+        it = [0]
+
+        def step():
+            i = it[0] % 2
+            it[0] += 1
+            fpn(sets[i], return_p6=True, out=outs[i], input_scales=scs[i])
+        ms = time_steps(step, steps, warmup=4)
+        if fpn.device_status() != 0:
+            raise RuntimeError(f"{name}: device pipeline timeout")
+        mult = 2.0 if fp8 else 1.0
+        esz = 1 if fp8 else 2
+        f_all = neck_flops(batch, chans, sizes)
+        b_all = neck_bytes(batch, chans, sizes, esz, 2)
+        t_roof = max(f_all / (peaks["bf16_tflops_sustained"] * mult * 1e12), b_all / (peaks["hbm_gbs"] * 1e9))
+        res[name] = {"images_per_s": round(batch * 1e3 / ms, 1), "ms_per_step": round(ms, 4),
+                     "batch": batch, "levels": [[batch, c, h, w] for c, (h, w) in zip(chans, sizes)],
+                     "dtype": "e4m3" if fp8 else str(dtype).replace("torch.", ""),
+                     "tflops": round(f_all / (ms * 1e-3) / 1e12, 1),
+                     "neck_frac_of_roofline": round(t_roof * 1e3 / ms, 4)}
+        del fpn, sets, outs
+        torch.cuda.empty_cache()
+
+    swin = (128, 256, 512, 1024)
+    neck("fp8_r50_640x640_16img", R50_CHANNELS, level_sizes(640, 640), 16, torch.float8_e4m3fn, 20)
+    neck("bf16_r50_1024x1024_8img", R50_CHANNELS, level_sizes(1024, 1024), 8, torch.bfloat16, 10)
+    neck("bf16_swin_1333x800_8img", swin, [(200, 334), (100, 167), (50, 84), (25, 42)], 8, torch.bfloat16, 20)
+    # single-level fused lateral + top-down add, fp32 NCHW (CUDA cores: TF32 would not meet 1e-4)
+    x = torch.randn(1, 512, 64, 64, device=dev, generator=gen)
+    c = torch.randn(1, 256, 32, 32, device=dev, generator=gen)
+    w = torch.randn(256, 512, device=dev, generator=gen) * (2.0 / 512) ** 0.5
+    b = torch.zeros(256, device=dev)
+    ms = time_steps(lambda: U.fpn_lateral_conv(x, w, b, c), 50, warmup=5)
+    flops = 2.0 * 64 * 64 * 256 * 512 + 9.0 * 64 * 64 * 256
+    nbytes = (x.numel() + c.numel() + w.numel() + b.numel() + 256 * 64 * 64) * 4
+    fp32_peak = U.get_peaks()["fp32_tflops"]
+    res["fp32_lateral_topdown_512x64x64"] = {
+        "us_per_call": round(ms * 1e3, 2), "gb_s": round(nbytes / (ms * 1e-3) / 1e9, 1),
+        "hbm_frac": round(nbytes / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+        "ffma_tflops": round(flops / (ms * 1e-3) / 1e12, 2),
+        "ffma_frac": round(flops / (ms * 1e-3) / 1e12 / fp32_peak, 4),
+        "ffma_peak_src": "nominal 80 TFLOP/s fp32 (no measured fp32 peak on this pool)",
+        "note": "includes one launch latency per call (a 14 MB op)"}
+    return res
+
+
+def e2e_ceiling(dev, h2d_bytes, d2h_bytes, steps, images_per_step):
+    """Plain pinned copies of the e2e line's bytes per step (host -> device and device -> host
+    on two streams, overlapped as HostPipeline overlaps them), no compute: the images/s that
+    host memory and PCIe allow this process."""
+    hin = torch.empty(h2d_bytes, dtype=torch.uint8, pin_memory=True)
+    hout = torch.empty(d2h_bytes, dtype=torch.uint8, pin_memory=True)
+    din = torch.empty(h2d_bytes, dtype=torch.uint8, device=dev)
+    dout = torch.empty(d2h_bytes, dtype=torch.uint8, device=dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    cur = torch.cuda.current_stream(dev)
+
+    def run(k):
+        ev = torch.cuda.Event()
+        ev.record(cur)
+        s_in.wait_event(ev)
+        s_out.wait_event(ev)
+        for _ in range(k):
+            with torch.cuda.stream(s_in):
+                din.copy_(hin, non_blocking=True)
+            with torch.cuda.stream(s_out):
+                hout.copy_(dout, non_blocking=True)
+        for s in (s_in, s_out):
+            e = torch.cuda.Event()
+            e.record(s)
+            cur.wait_event(e)
+    run(2)
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(cur)
+    run(steps)
+    e1.record(cur)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    return ms, images_per_step * steps
 
 
 def measured_peaks():
@@ -335,6 +473,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-roofline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the other configurations' shards timed after the headline")
     ap.add_argument("--schedule", choices=["fused", "split", "serial"], default="split",
                     help="one persistent neck kernel, per-level kernels on two streams, or the "
                          "per-level kernels one after the other on one stream")
@@ -430,7 +570,9 @@ def main():
     if world > 1:
         dist.barrier()
     clk = clocks.stop()
-    ms, images = job_throughput(e0.elapsed_time(e1), B * args.steps, world, dev)
+    ms_local = e0.elapsed_time(e1)
+    ms, images = job_throughput(ms_local, B * args.steps, world, dev)
+    ranks_ms = per_rank_ms(ms_local / args.steps, world, dev)
     status = fpn.device_status()
     value = images / (ms / 1e3)
     ms_per_step = ms / args.steps
@@ -467,6 +609,13 @@ def main():
         e2e = {"value": e_images / (ems / 1e3), "unit": "images/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "steps": n_e2e,
                "api": "unified_fpn.HostPipeline (copy-in / neck / copy-out overlapped across steps)"}
+        if world > 1:
+            dist.barrier()
+        cms, c_images = e2e_ceiling(dev, h2d, d2h, n_e2e, B)
+        cms, c_images = job_throughput(cms, c_images, world, dev)
+        e2e["ceiling"] = {"value": c_images / (cms / 1e3), "unit": "images/s",
+                          "what": "the same bytes as plain pinned cudaMemcpyAsync H2D + D2H on two "
+                                  "overlapped streams, no compute (host memory / PCIe bound)"}
 
     # ---------------------------------------------------------------- roofline of the dominant kernel
     roofline = None
@@ -532,6 +681,10 @@ def main():
         timeline = {k: (round(v, 1) if v is not None else None)
                     for k, v in fpn.neck_timeline(feats[0]).items()}
 
+    extra = None
+    if not args.no_extra and world == 1 and not fp8 and not args.no_roofline:
+        extra = extra_workloads(dev, peaks)
+
     cpu = None
     if rank == 0 and not args.no_cpu_baseline and world == 1:
         cpu = cpu_baseline(image=(args.height, args.width))
@@ -553,8 +706,12 @@ def main():
                        "parallelism": f"dp{world} batch shards, no collective on the data path"},
             "clocks": clk, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
             "schedule": args.schedule, "neck_timeline_us": timeline,
-            "roofline": roofline, "kernel_time_share": kernel_share, "cpu_baseline": cpu,
-            "device_status": status,
+            "roofline": roofline, "kernel_time_share": kernel_share,
+            "kernel_time_share_what": "device time per stage of one forward with the stages serialised "
+                                      "on one stream (replayed as a CUDA graph, events between stages; "
+                                      "the concurrent schedule overlaps them)",
+            "cpu_baseline": cpu,
+            "device_status": status, "per_rank_ms_per_step": ranks_ms, "extra": extra,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -58,6 +58,9 @@ class __attribute__((visibility("default"))) UnifiedFPNCore {
 
   // Time every kernel of the next forward() with CUDA events (serialises the
   // schedule; synchronises the stream at the end of that forward).
+  // Graph cache counters: [0] pointer sets captured into a graph, [1] graph replays,
+  // [2] forwards launched directly (a pointer set's first use), [3] graphs cached now.
+  void graph_stats(long long* out4) const;
   void set_profiling(bool enable);
   // Record the fused neck kernel's device timeline during the next forward() (launched
   // directly, then the stream is synchronised).  get_neck_trace returns globaltimer ns:

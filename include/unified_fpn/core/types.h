@@ -177,6 +177,11 @@ struct FPNKernelConfig {
   // lateral runs in its own kernel and ignores its entry): 1, 2 or 4.  A long K loop (the P5
   // lateral's 2048 channels) otherwise holds one SM per tile for its whole weight stream.
   int lateral_ksplit[4] = {1, 1, 1, 1};
+  // Self-test of the device's bounded waits (0 = off): on the fused schedule, the P2 3x3
+  // waits for a lateral tile that never comes, with a limit of this many microseconds, so
+  // the forward ends with status kDevTimeoutDependency (outputs undefined) and the engine
+  // must recover after device_status(reset).  No fault, trap or hang is involved.
+  int test_stall_dependency_us = 0;
 };
 
 struct FPNWeights {

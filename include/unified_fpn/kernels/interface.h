@@ -222,6 +222,11 @@ cudaError_t tc_set_channel_slices(TcPlan& plan, const void* w, int K, int slices
 // Tiling with the fewest padded pixels for an H x W map (ties: 16 wide).
 Conv3x3Tiling default_tiling(int H, int W);
 
+// Peaks the profiled forward reports its utilisation against (engine.cu): dense 16-bit
+// tensor FLOP/s, fp32 FLOP/s, HBM bytes/s; values <= 0 keep the current one.
+void set_device_peaks(double tensor_flops, double fp32_flops, double hbm_bytes);
+void get_device_peaks(double* out3);
+
 // ---- whole-neck persistent kernel (one launch for all 4 laterals and 4 3x3 convs)
 struct NeckLevel {
   const void* x;        // C_l, NHWC [N][H][W][Cin]
@@ -274,6 +279,11 @@ cudaError_t plan_neck_jobs(NeckPlan& plan, DType dt, int N, const NeckLevel* lev
                            const NeckJobSpec* specs, int num_specs, int* sched, int* status,
                            int max_ctas, unsigned long long* trace = nullptr);
 cudaError_t launch_neck(const NeckPlan& plan, cudaStream_t s, LaunchOpts opts = LaunchOpts());
+// Self-test of the bounded waits: in a planned launch, the 3x3 job of `level` waits for one
+// more lateral tile than its level has (a count nothing reaches) with a wait limit of
+// wait_ns; its tiles then give up, record kDevTimeoutDependency (0x105) in the status word
+// and the kernel ends normally (copies drained, TMEM freed, schedule counters reset).
+cudaError_t neck_plan_stall_dependency(NeckPlan& plan, int level, unsigned long long wait_ns);
 cudaError_t launch_tc(const TcPlan& plan, cudaStream_t s, LaunchOpts opts = LaunchOpts());
 
 // ---- backward pass (backward.cu).  Reference: src/training/backward/lateral_conv_backward.cu

@@ -38,6 +38,15 @@ extern "C" {
 #define UFPN_DTYPE_BF16 2
 #define UFPN_DTYPE_E4M3 6
 
+/* Device status words (ufpn_device_status, ufpn_core_device_status): the first bounded wait
+ * that gave up in a launch records which role it was; 0 = no error.  Each replaces one of
+ * the reference's exit() paths (include/unified_fpn/core/types.h:140-206). */
+#define UFPN_DEV_TIMEOUT_PRODUCER 0x101   /* TMA producer waiting for a free stage */
+#define UFPN_DEV_TIMEOUT_MMA 0x102        /* MMA issuer waiting for operands / accumulator */
+#define UFPN_DEV_TIMEOUT_EPILOGUE 0x103   /* epilogue waiting for an accumulator */
+#define UFPN_DEV_TIMEOUT_DRAIN 0x104      /* teardown waiting for copies in flight */
+#define UFPN_DEV_TIMEOUT_DEPENDENCY 0x105 /* one-launch neck: a level dependency not met */
+
 #define UFPN_LAYOUT_NCHW 0 /* torch contiguous */
 #define UFPN_LAYOUT_NHWC 1 /* torch channels_last */
 
@@ -45,6 +54,13 @@ extern "C" {
 const char* ufpn_last_error(void);
 /* Library version, major * 10000 + minor * 100 + patch. */
 int ufpn_version(void);
+/* Peaks that utilisation figures (ufpn_core_get_performance_metrics, UnifiedFPN.benchmark)
+ * are reported against: dense 16-bit tensor TFLOP/s (e4m3 counts twice it), fp32 CUDA-core
+ * TFLOP/s, HBM GB/s.  Nominal B200 figures (2250, 80, 8000) until set; a value of 0 keeps
+ * the current one.  No reference counterpart (the reference divided by fixed figures,
+ * python/fpn_pytorch.cpp:160-166).  ufpn_get_peaks writes the three current values. */
+int ufpn_set_peaks(double tensor_tflops, double fp32_tflops, double hbm_gbs);
+int ufpn_get_peaks(double* out3);
 /* Reads (and with reset != 0 clears) the status word the tensor-core kernels of
  * the standalone entry points write when a pipeline wait times out on the
  * current device; 0 = no error.  Synchronises the device. */
@@ -120,11 +136,23 @@ int ufpn_core_set_schedule_options(ufpn_core* core, int programmatic_launch, int
  *   "ksplit_p3", "ksplit_p4", "ksplit_p5"
  *                       1/2/4 units per lateral tile over K in that launch (a last-arriving
  *                            unit sums the fp32 partials in a fixed order: deterministic)
+ *   "test_stall_dependency_us"  0..1000000  self-test of the device's bounded waits (0 =
+ *                            off): on the fused schedule the P2 3x3 waits for a lateral tile
+ *                            that never comes, for this many microseconds, then the forward
+ *                            ends with device status 0x105 (outputs undefined); clear it with
+ *                            ufpn_core_device_status(reset = 1)
  *   "programmatic_launch", "chain_priority", "merge_two_levels", "single_stream",
  *   "fused_neck_kernel" 0/1  as ufpn_core_set_schedule / ufpn_core_set_schedule_options
  * Unknown names and values return UFPN_ERR_INVALID_ARG. */
 int ufpn_core_set_option(ufpn_core* core, const char* name, int value);
 int ufpn_core_get_option(const ufpn_core* core, const char* name, int* value);
+
+/* Graph cache of the forward (no reference counterpart; the reference launched every kernel
+ * each call and synchronised the host, fpn_engine.cu:191-245).  A forward's pointer set
+ * (inputs, outputs, P6, e4m3 scales) is captured into a CUDA graph on its second use and
+ * replayed after that (up to 8 sets cached, oldest evicted); its first use launches the
+ * kernels directly.  out4: [0] captures, [1] replays, [2] direct forwards, [3] cached now. */
+int ufpn_core_graph_stats(const ufpn_core* core, long long* out4);
 
 size_t ufpn_core_get_memory_usage(const ufpn_core* core);
 /* fpn_pytorch.cpp:171-187 (get_performance_breakdown): kernel_times_ms[8], metrics[5] =

@@ -448,3 +448,108 @@ def test_schedule_option_api_errors(cuda_device):
         fpn.set_option("no_such_option", 1)
     with pytest.raises(RuntimeError):
         fpn.set_option("ksplit_p5", 3)
+
+
+def test_bounded_wait_runs_out_and_the_engine_recovers(cuda_device):
+    """A device wait that runs out: on the fused schedule the P2 3x3 tiles wait for one more
+    P2 lateral tile than exists, with a 5 ms limit.  The forward ends by itself within the
+    limit (no trap, no hang), the status word names the dependency wait, the reset clears it
+    together with the schedule counters, and the next forward matches the oracle again."""
+    import time
+    import unified_fpn as U
+    from unified_fpn import _lib
+    chans, sizes = O.R50_CHANNELS, O.level_sizes(160, 224)
+    host = O.make_features(2, chans, sizes, seed=97)
+    wts = O.make_weights(chans, seed=98, bias_scale=0.1)
+    fpn = U.UnifiedFPN()
+    fpn.set_schedule(fused_neck_kernel=True)
+    fpn.initialize_weights(wts.lat_w, wts.lat_b, wts.out_w, wts.out_b)
+    xin = [_cl(f.to(torch.bfloat16).cuda()) for f in host]
+    rw = O.NeckWeights([O.round_to(w, torch.bfloat16) for w in wts.lat_w], wts.lat_b,
+                       [O.round_to(w, torch.bfloat16) for w in wts.out_w], wts.out_b)
+    ref = O.fpn_neck([O.round_to(f, torch.bfloat16) for f in host], rw)
+    _check([o.clone() for o in _run(fpn, xin)], ref, torch.bfloat16)
+    assert fpn.device_status() == 0
+
+    fpn.set_option("test_stall_dependency_us", 5000)
+    t0 = time.perf_counter()
+    _run(fpn, xin)
+    elapsed = time.perf_counter() - t0
+    assert elapsed < 1.0, elapsed  # ended by itself, about 5 ms after the P2 3x3 tiles began
+    assert fpn.device_status(reset=False) == _lib.DEV_TIMEOUT_DEPENDENCY
+    assert fpn.device_status(reset=True) == _lib.DEV_TIMEOUT_DEPENDENCY
+    assert fpn.device_status() == 0  # cleared
+
+    fpn.set_option("test_stall_dependency_us", 0)
+    for _ in range(2):  # the schedule counters start at zero again
+        outs = [o.clone() for o in _run(fpn, xin)]
+        assert fpn.device_status() == 0
+        _check(outs, ref, torch.bfloat16)
+
+
+def test_helpers_drop_in(cuda_device, tmp_path):
+    """The reference package's helpers with its signatures and result keys
+    (python/__init__.py:82-257) and UnifiedFPN.benchmark (fpn_pytorch.cpp:139-169)."""
+    import json
+    import unified_fpn as U
+    sizes = O.level_sizes(256, 384)
+    feats = [_cl(f.to(torch.bfloat16).cuda()) for f in O.make_features(2, O.R50_CHANNELS, sizes, seed=5)]
+    fpn = U.UnifiedFPN()
+
+    avg_ms, gbs, util = fpn.benchmark(feats, num_iterations=5)
+    assert avg_ms > 0 and gbs > 0 and 0 < util < 1.5
+
+    res = U.benchmark_fpn(feats, num_iterations=5, warmup_iterations=2, fpn=fpn)
+    for key in ("avg_time_ms", "throughput_fps", "memory_bandwidth_gb_s", "compute_utilization",
+                "memory_usage_mb", "detailed_metrics"):
+        assert key in res, key
+    assert res["avg_time_ms"] > 0 and res["throughput_fps"] == pytest.approx(1000.0 / res["avg_time_ms"])
+    assert res["images_per_s"] == pytest.approx(2 * res["throughput_fps"])
+
+    out = tmp_path / "fpn_profile.json"
+    prof = U.profile_fpn(feats, str(out), fpn=fpn)
+    saved = json.loads(out.read_text())
+    for key in ("kernel_times_ms", "total_time_ms", "memory_bandwidth_gb_s", "compute_utilization",
+                "peak_memory_mb", "num_kernel_launches"):
+        assert key in saved and saved[key] == prof[key], key
+    assert len(saved["kernel_times_ms"]) == 8 and min(saved["kernel_times_ms"]) >= 0
+    assert saved["total_time_ms"] >= sum(saved["kernel_times_ms"]) * 0.99
+    # utilisation is against the peaks the library reports (measured when available)
+    pk = U.get_peaks()
+    flops = sum(2.0 * 2 * h * w * 256 * (c + 9 * 256) for c, (h, w) in zip(O.R50_CHANNELS, sizes))
+    assert saved["compute_utilization"] == pytest.approx(
+        flops / (saved["total_time_ms"] * 1e-3) / (pk["tensor_tflops"] * 1e12), rel=1e-3)
+    assert U.profile_fpn(feats, None, fpn=fpn)["num_kernel_launches"] == saved["num_kernel_launches"]
+
+    info = U.get_device_info()
+    for key in ("device_name", "compute_capability", "total_memory_gb", "multiprocessor_count",
+                "max_threads_per_block", "max_threads_per_multiprocessor", "memory_clock_rate_mhz",
+                "memory_bus_width_bits", "l2_cache_size_mb", "theoretical_bandwidth_gb_s"):
+        assert key in info, key
+    assert info["compute_capability"] == "10.0" and info["multiprocessor_count"] > 0
+    assert U.check_installation() is True
+
+
+def test_graph_cache_with_fresh_outputs_every_call(cuda_device):
+    """The drop-in call fpn(feats) allocates new outputs each time (as the reference's binding
+    did, fpn_pytorch.cpp:113-136).  Kept alive, every call has a new pointer set: each runs as
+    direct launches (no capture, nothing evicted), bitwise what the graph replays give."""
+    import unified_fpn as U
+    feats = [_cl(f.to(torch.bfloat16).cuda()) for f in O.make_features(1, O.R50_CHANNELS, O.level_sizes(128, 192), seed=3)]
+    fpn = U.UnifiedFPN()
+    ref = _run(fpn, feats)  # kept alive: the allocator cannot hand its memory out again
+    kept = [fpn(feats, return_p6=True) for _ in range(20)]
+    torch.cuda.synchronize()
+    st = fpn.graph_stats()
+    assert st["captures"] == 0 and st["direct"] == 21, st
+    for outs in kept:
+        assert all(torch.equal(a, b) for a, b in zip(outs, ref))
+    # a repeating pointer set: captured on its second use, replayed from then on
+    out = [torch.empty_like(r) for r in ref]
+    for _ in range(5):
+        fpn(feats, return_p6=True, out=out)
+    torch.cuda.synchronize()
+    st2 = fpn.graph_stats()
+    assert st2["captures"] == 1 and st2["replays"] == 3 and st2["direct"] == 22, st2
+    assert all(torch.equal(a, b) for a, b in zip(out, ref))
+    assert fpn.device_status() == 0
