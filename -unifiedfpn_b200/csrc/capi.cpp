@@ -1,6 +1,8 @@
 // extern "C" boundary of libunified_fpn_b200.so (declared in include/unified_fpn_c.h).
 // Every entry point catches exceptions, stores a message for ufpn_last_error()
 // and returns a status code; nothing here calls exit().
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <chrono>
@@ -300,75 +302,24 @@ int ufpn_core_set_schedule_options(ufpn_core* core, int programmatic_launch, int
   });
 }
 
-namespace {
-// Named integer options of the engine's schedule (ufpn_core_set_option): the field of
-// FPNKernelConfig each name addresses and its accepted values.
-struct OptionField {
-  const char* name;
-  int* (*field)(FPNKernelConfig&);
-  bool (*valid)(int);
-};
-bool valid_bool(int v) { return v == 0 || v == 1; }
-bool valid_ksplit(int v) { return v == 1 || v == 2 || v == 4; }
-bool valid_stall(int v) { return v >= 0 && v <= 1000000; }  // at most 1 s
-const OptionField kOptions[] = {
-    {"ksplit_p3", [](FPNKernelConfig& c) { return &c.lateral_ksplit[1]; }, valid_ksplit},
-    {"ksplit_p4", [](FPNKernelConfig& c) { return &c.lateral_ksplit[2]; }, valid_ksplit},
-    {"ksplit_p5", [](FPNKernelConfig& c) { return &c.lateral_ksplit[3]; }, valid_ksplit},
-    {"test_stall_dependency_us", [](FPNKernelConfig& c) { return &c.test_stall_dependency_us; },
-     valid_stall},
-};
-// Boolean options (stored as bool in FPNKernelConfig).
-struct BoolOption {
-  const char* name;
-  bool FPNKernelConfig::*field;
-};
-const BoolOption kBoolOptions[] = {
-    {"grouped_topdown", &FPNKernelConfig::grouped_topdown},
-    {"programmatic_launch", &FPNKernelConfig::programmatic_launch},
-    {"chain_priority", &FPNKernelConfig::chain_priority},
-    {"merge_two_levels", &FPNKernelConfig::merge_two_levels},
-    {"single_stream", &FPNKernelConfig::single_stream},
-    {"fused_neck_kernel", &FPNKernelConfig::fused_neck_kernel},
-};
-}  // namespace
-
 int ufpn_core_set_option(ufpn_core* core, const char* name, int value) {
   if (!core || !name) return fail(UFPN_ERR_INVALID_ARG, "NULL core or name");
-  return guarded([&] {
-    FPNKernelConfig c = core->core.get_kernel_config();
-    for (const auto& o : kOptions) {
-      if (std::strcmp(o.name, name) != 0) continue;
-      if (!o.valid(value)) return fail(UFPN_ERR_INVALID_ARG, std::string("bad value for ") + name);
-      *o.field(c) = value;
-      core->core.set_kernel_config(c);
-      return UFPN_OK;
-    }
-    for (const auto& o : kBoolOptions) {
-      if (std::strcmp(o.name, name) != 0) continue;
-      if (!valid_bool(value)) return fail(UFPN_ERR_INVALID_ARG, std::string("bad value for ") + name);
-      c.*o.field = value != 0;
-      core->core.set_kernel_config(c);
-      return UFPN_OK;
-    }
-    return fail(UFPN_ERR_INVALID_ARG, std::string("unknown option ") + name);
-  });
+  try {
+    core->core.set_option(name, value);
+  } catch (const std::exception& e) {
+    return fail(UFPN_ERR_INVALID_ARG, e.what());  // unknown name or value
+  }
+  return UFPN_OK;
 }
 
 int ufpn_core_get_option(const ufpn_core* core, const char* name, int* value) {
   if (!core || !name || !value) return fail(UFPN_ERR_INVALID_ARG, "NULL argument");
-  FPNKernelConfig c = core->core.get_kernel_config();
-  for (const auto& o : kOptions)
-    if (std::strcmp(o.name, name) == 0) {
-      *value = *o.field(c);
-      return UFPN_OK;
-    }
-  for (const auto& o : kBoolOptions)
-    if (std::strcmp(o.name, name) == 0) {
-      *value = (c.*o.field) ? 1 : 0;
-      return UFPN_OK;
-    }
-  return fail(UFPN_ERR_INVALID_ARG, std::string("unknown option ") + name);
+  try {
+    *value = core->core.get_option(name);
+  } catch (const std::exception& e) {
+    return fail(UFPN_ERR_INVALID_ARG, e.what());
+  }
+  return UFPN_OK;
 }
 
 int ufpn_core_graph_stats(const ufpn_core* core, long long* out4) {
@@ -404,10 +355,16 @@ int ufpn_core_set_profiling(ufpn_core* core, int enable) {
 
 int ufpn_core_autotune(ufpn_core* core, const void* const* inputs, void* const* outputs,
                        void* p6, void* stream, int iterations) {
+  return ufpn_core_autotune_scaled(core, inputs, nullptr, outputs, p6, stream, iterations);
+}
+
+int ufpn_core_autotune_scaled(ufpn_core* core, const void* const* inputs,
+                              const float* const* input_scales, void* const* outputs, void* p6,
+                              void* stream, int iterations) {
   if (!core || !inputs || !outputs) return fail(UFPN_ERR_INVALID_ARG, "NULL");
   return guarded([&] {
     g_last_error = core->core.autotune(inputs, outputs, p6, static_cast<cudaStream_t>(stream),
-                                       iterations);
+                                       iterations, input_scales);
     return UFPN_OK;
   });
 }
@@ -1217,10 +1174,110 @@ int export_upsample_profiling_data(void* engine, const char* filename) {
 }
 
 // ------------------------------------------------------------------ autotuner C ABI
+}  // extern "C"
+
+namespace ufpn {
+void record_lateral_tiling(DType dt, int N, int cin, int H, int W, int tile_w);  // engine.cu
+}
 namespace {
 std::mutex g_tune_mu;
 std::map<std::tuple<int, int, int, int, int>, TuningResult> g_tune_results;
+
+// Seeded pseudo-random 16-bit values in [-1, 1) (hash of the index): tuning inputs that are
+// not all zero, made on the device.
+template <typename T>
+__global__ void tune_fill_kernel(T* p, size_t n, uint32_t seed, float scale) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    uint32_t h = static_cast<uint32_t>(i) * 2654435761u ^ seed;
+    h ^= h >> 15;
+    h *= 2246822519u;
+    h ^= h >> 13;
+    p[i] = static_cast<T>((static_cast<float>(h & 0xFFFFu) / 32768.f - 1.f) * scale);
+  }
+}
+template <typename T>
+void tune_fill(void* p, size_t n, uint32_t seed, float scale, cudaStream_t s) {
+  tune_fill_kernel<T><<<1024, 256, 0, s>>>(static_cast<T*>(p), n, seed, scale);
+}
 }  // namespace
+
+extern "C" {
+
+int ufpn_autotune_lateral(int dtype, int batch_size, int in_channels, int height, int width,
+                          void* stream, TuningResult* out) {
+  DType dt;
+  if (!parse_dtype(dtype, &dt) || (dt != DType::BF16 && dt != DType::F16))
+    return fail(UFPN_ERR_UNSUPPORTED, "the lateral tuner takes bf16 or fp16");
+  if (!out || batch_size <= 0 || in_channels <= 0 || in_channels % 8 != 0 || height <= 0 || width <= 0)
+    return fail(UFPN_ERR_INVALID_ARG, "need positive sizes, Cin % 8 == 0 and a result pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t px = static_cast<size_t>(batch_size) * height * width;
+  void *x = nullptr, *w = nullptr, *o = nullptr;
+  float* b = nullptr;
+  TuningResult res{};
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  bool ok = cudaMalloc(&x, px * in_channels * 2) == cudaSuccess &&
+            cudaMalloc(&w, static_cast<size_t>(256) * in_channels * 2) == cudaSuccess &&
+            cudaMalloc(&o, px * 256 * 2) == cudaSuccess &&
+            cudaMalloc(&b, 256 * sizeof(float)) == cudaSuccess &&
+            cudaEventCreate(&e0) == cudaSuccess && cudaEventCreate(&e1) == cudaSuccess;
+  float best = -1.f;
+  if (ok) {
+    if (dt == DType::BF16) {
+      tune_fill<__nv_bfloat16>(x, px * in_channels, 1u, 1.f, s);
+      tune_fill<__nv_bfloat16>(w, static_cast<size_t>(256) * in_channels, 2u, 0.05f, s);
+    } else {
+      tune_fill<__half>(x, px * in_channels, 1u, 1.f, s);
+      tune_fill<__half>(w, static_cast<size_t>(256) * in_channels, 2u, 0.05f, s);
+    }
+    cudaMemsetAsync(b, 0, 256 * sizeof(float), s);
+    // candidates: every lateral tile shape of 128 pixels (width 8..128) that is not mostly
+    // padding, each timed on the caller's stream (10 launches after one warm-up)
+    for (int tw : {8, 16, 32, 64, 128}) {
+      if (tw > 2 * width && tw != 8) continue;
+      ufpn::Conv3x3Tiling t;
+      t.tile_w = tw;
+      t.tile_h = 128 / tw;
+      ufpn::TcPlan plan;
+      if (ufpn::plan_tc_lateral(plan, dt, x, w, b, nullptr, o, batch_size, in_channels, height,
+                                width, 0, 0, t, device_status_word(), 0) != cudaSuccess)
+        continue;
+      if (ufpn::launch_tc(plan, s) != cudaSuccess) break;
+      cudaEventRecord(e0, s);
+      for (int i = 0; i < 10; ++i) ufpn::launch_tc(plan, s);
+      cudaEventRecord(e1, s);
+      if (cudaEventSynchronize(e1) != cudaSuccess) break;
+      float ms = 0.f;
+      cudaEventElapsedTime(&ms, e0, e1);
+      ms /= 10.f;
+      if (best < 0 || ms < best) {
+        best = ms;
+        res.tile_w = tw;
+        res.tile_h = 128 / tw;
+        res.num_ctas = plan.grid;
+      }
+    }
+    ok = best > 0;
+  }
+  if (e0) cudaEventDestroy(e0);
+  if (e1) cudaEventDestroy(e1);
+  cudaFree(x);
+  cudaFree(w);
+  cudaFree(o);
+  cudaFree(b);
+  if (!ok) return fail(UFPN_ERR_CUDA, "lateral tuning: allocation or launch failed");
+  res.time_ms = best;
+  const double flops = 2.0 * px * 256 * in_channels;
+  const double bytes = (px * (in_channels + 256) + 256.0 * in_channels) * 2;
+  res.performance_gflops = static_cast<float>(flops / (best * 1e-3) / 1e9);
+  res.memory_bandwidth_gb_s = static_cast<float>(bytes / (best * 1e-3) / 1e9);
+  std::snprintf(res.architecture_name, sizeof(res.architecture_name), "sm_100a");
+  // engines configured for this shape afterwards start from the tuned tile shape
+  ufpn::record_lateral_tiling(dt, batch_size, in_channels, height, width, res.tile_w);
+  *out = res;
+  return UFPN_OK;
+}
 
 TuningResult* fpn_auto_tune_lateral_conv(int batch_size, int in_channels, int out_channels,
                                          int height, int width) {
@@ -1233,60 +1290,11 @@ TuningResult* fpn_auto_tune_lateral_conv(int batch_size, int in_channels, int ou
   auto key = std::make_tuple(batch_size, in_channels, out_channels, height, width);
   auto it = g_tune_results.find(key);
   if (it != g_tune_results.end()) return &it->second;
-  const size_t px = static_cast<size_t>(batch_size) * height * width;
-  void *x = nullptr, *w = nullptr, *o = nullptr;
-  float* b = nullptr;
   TuningResult res{};
-  bool ok = cudaMalloc(&x, px * in_channels * 2) == cudaSuccess &&
-            cudaMalloc(&w, static_cast<size_t>(256) * in_channels * 2) == cudaSuccess &&
-            cudaMalloc(&o, px * 256 * 2) == cudaSuccess &&
-            cudaMalloc(&b, 256 * sizeof(float)) == cudaSuccess;
-  if (ok) {
-    cudaMemset(x, 0, px * in_channels * 2);
-    cudaMemset(w, 0, static_cast<size_t>(256) * in_channels * 2);
-    cudaMemset(b, 0, 256 * sizeof(float));
-    const int sms = ufpn::sm_count();
-    cudaEvent_t e0, e1;
-    cudaEventCreate(&e0);
-    cudaEventCreate(&e1);
-    float best = -1.f;
-    for (int ctas : {sms, sms / 2, 2 * sms / 3}) {
-      ufpn::TcPlan plan;
-      if (ufpn::plan_tc_lateral(plan, DType::BF16, x, w, b, nullptr, o, batch_size, in_channels,
-                                height, width, 0, 0, ufpn::default_tiling(height, width),
-                                device_status_word(), ctas) != cudaSuccess)
-        continue;
-      ufpn::launch_tc(plan, 0);
-      cudaEventRecord(e0, 0);
-      for (int i = 0; i < 10; ++i) ufpn::launch_tc(plan, 0);
-      cudaEventRecord(e1, 0);
-      if (cudaEventSynchronize(e1) != cudaSuccess) break;
-      float ms = 0.f;
-      cudaEventElapsedTime(&ms, e0, e1);
-      ms /= 10.f;
-      if (best < 0 || ms < best) {
-        best = ms;
-        res.num_ctas = plan.grid;
-      }
-    }
-    cudaEventDestroy(e0);
-    cudaEventDestroy(e1);
-    res.time_ms = best;
-    const double flops = 2.0 * px * 256 * in_channels;
-    const double bytes = (px * (in_channels + 256) + 256.0 * in_channels) * 2;
-    res.performance_gflops = best > 0 ? static_cast<float>(flops / (best * 1e-3) / 1e9) : 0.f;
-    res.memory_bandwidth_gb_s = best > 0 ? static_cast<float>(bytes / (best * 1e-3) / 1e9) : 0.f;
-    std::snprintf(res.architecture_name, sizeof(res.architecture_name), "sm_100a");
-    ok = best > 0;
-  }
-  cudaFree(x);
-  cudaFree(w);
-  cudaFree(o);
-  cudaFree(b);
-  if (!ok) {
-    g_last_error = "fpn_auto_tune_lateral_conv: allocation or launch failed";
+  // (the reference's signature has no stream: the calling thread's default stream)
+  if (ufpn_autotune_lateral(UFPN_DTYPE_BF16, batch_size, in_channels, height, width,
+                            cudaStreamPerThread, &res) != UFPN_OK)
     return nullptr;
-  }
   auto ins = g_tune_results.emplace(key, res);
   return &ins.first->second;
 }

@@ -20,6 +20,8 @@
 #include <cstdio>
 #include <cstring>
 #include <fstream>
+#include <functional>
+#include <mutex>
 #include <map>
 #include <sstream>
 #include <string>
@@ -96,6 +98,32 @@ void get_device_peaks(double* out3) {
   out3[1] = g_peak_fp32.load();
   out3[2] = g_peak_hbm.load();
 }
+
+// Lateral tile shapes chosen by the standalone lateral tuner (fpn_auto_tune_lateral_conv),
+// process-wide, keyed by (dtype, batch, Cin, H, W); an engine configuring that geometry
+// starts from them (its own whole-neck tuning, when present, takes precedence).
+namespace {
+std::mutex g_lat_mu;
+std::map<std::string, int> g_lat_tuned;  // key -> tile width
+std::string lat_key(DType dt, int N, int cin, int H, int W) {
+  std::ostringstream k;
+  k << static_cast<int>(dt) << "/" << N << "x" << cin << "x" << H << "x" << W;
+  return k.str();
+}
+}  // namespace
+void record_lateral_tiling(DType dt, int N, int cin, int H, int W, int tile_w) {
+  std::lock_guard<std::mutex> lk(g_lat_mu);
+  g_lat_tuned[lat_key(dt, N, cin, H, W)] = tile_w;
+}
+bool lateral_tiling_for(DType dt, int N, int cin, int H, int W, Conv3x3Tiling* t) {
+  std::lock_guard<std::mutex> lk(g_lat_mu);
+  auto it = g_lat_tuned.find(lat_key(dt, N, cin, H, W));
+  if (it == g_lat_tuned.end()) return false;
+  t->tile_w = it->second;
+  t->tile_h = 128 / it->second;
+  t->halo = t->pair = false;
+  return true;
+}
 }  // namespace ufpn
 
 struct UnifiedFPNCore::Impl {
@@ -134,6 +162,7 @@ struct UnifiedFPNCore::Impl {
   int* split_sem = nullptr;
   int split_sem_off[4] = {};
   int split_alloc[4] = {1, 1, 1, 1};
+  Conv3x3Tiling split_tiling[4];  // lateral tilings the split workspace was sized for
   size_t split_bytes = 0;
   const float* in_scale[4] = {};  // e4m3: scales of the current forward's inputs
   unsigned* fp8_amax = nullptr;   // e4m3: [4][N] per-image absmax of M_l (fp32 bits)
@@ -161,6 +190,10 @@ struct UnifiedFPNCore::Impl {
   FPNKernelConfig cfg;
   Conv3x3Tiling tiling[4];
   bool tiling_tuned[4] = {};
+  Conv3x3Tiling lat_tiling[4];  // lateral tile shape per level (tuned or the least padding)
+  int wb_tile_w = 0;            // lateral tile width the Wb table was built for
+  bool p2_pair = false;         // 16-bit P2 lateral on CTA pairs (resident weight halves)
+  int merge_units = 0;          // units per block of the merge kernels (0: automatic)
   bool profiling = false;
   FPNPerformanceMetrics metrics{};
   struct GraphEntry {
@@ -181,7 +214,9 @@ struct UnifiedFPNCore::Impl {
   };
   std::vector<SeenKey> seen_once;
   long long stat_captures = 0, stat_replays = 0, stat_direct = 0;
-  std::map<std::string, std::pair<int, float>> tuning_db;  // key -> (tile_w, ms)
+  std::map<std::string, std::pair<int, float>> tuning_db;  // v1: key -> (3x3 tile_w, ms)
+  // v2 (whole-neck tuning): geometry key -> knob values and the tuned forward time
+  std::map<std::string, std::pair<std::map<std::string, int>, float>> tuning_db2;
 
   ~Impl() { release_all(); }
 
@@ -223,6 +258,55 @@ struct UnifiedFPNCore::Impl {
     workspace_bytes -= split_bytes;
     split_bytes = 0;
   }
+  // The P2 lateral's top-down weights (tensor-core k-block) depend only on the geometry and
+  // the lateral's tile shape: built at configuration and again when the tile shape changes.
+  size_t wb_bytes = 0;
+  void build_wb_table() {
+    cudaFree(wb_table);
+    wb_table = nullptr;
+    workspace_bytes -= wb_bytes;
+    wb_bytes = 0;
+    wb_tile_w = 0;
+    if (!configured || !tensor_core_path()) return;
+    const size_t tb = ufpn::tc_wb_table_bytes(H[0], W[0], H[1], W[1], lat_tiling[0]);
+    wb_tile_w = lat_tiling[0].tile_w;
+    if (tb == 0) return;  // taps beyond one box: the lateral reads them from global memory
+    check(cudaMalloc(&wb_table, tb), "workspace");
+    check(ufpn::tc_build_wb_table(dtype, H[0], W[0], H[1], W[1], lat_tiling[0], wb_table, setup),
+          "build bilinear weight table");
+    check(cudaStreamSynchronize(setup), "build bilinear weight table");
+    wb_bytes = tb;
+    workspace_bytes += tb;
+  }
+  // Buffers the current knob settings need, allocated before any capture.
+  void ensure_plan_buffers() {
+    if (!tensor_core_path()) return;
+    if (wb_tile_w != lat_tiling[0].tile_w) {
+      release_graphs();
+      build_wb_table();
+    }
+    if (cfg.merge_two_levels && !lat4_raw && H[3] <= H[2] && W[3] <= W[2] && H[2] <= H[1] &&
+        W[2] <= W[1]) {
+      release_graphs();
+      const size_t bytes = static_cast<size_t>(batch) * H[2] * W[2] * cout * 2;
+      check(cudaMalloc(&lat4_raw, bytes), "workspace");
+      workspace_bytes += bytes;
+    }
+    ensure_split_workspace();
+  }
+  // Key of this geometry in the whole-neck tuning cache: dtype, layout, batch, every level's
+  // shape, the SM count and the driver version.
+  std::string geometry_key() const {
+    std::ostringstream k;
+    int drv = 0;
+    cudaDriverGetVersion(&drv);
+    k << "neck/dt" << static_cast<int>(dtype) << "/lay" << static_cast<int>(layout) << "/b" << batch;
+    for (int l = 0; l < 4; ++l) k << "/" << cin[l] << "x" << H[l] << "x" << W[l];
+    k << "/sm" << ufpn::sm_count() << "/drv" << drv;
+    return k.str();
+  }
+  void apply_tuning_db2();  // (defined with the option table)
+
   // Units per tile of level l's lateral in the grouped launch (1 when the level does not
   // split or its K loop is too short for the configured split).
   int lateral_ksplit(int l) const {
@@ -236,14 +320,15 @@ struct UnifiedFPNCore::Impl {
     if (!tensor_core_path() || dtype == DType::E4M3) return;
     bool same = split_sem != nullptr || (lateral_ksplit(1) == 1 && lateral_ksplit(2) == 1 &&
                                          lateral_ksplit(3) == 1);
-    for (int l = 1; l < 4 && same && split_sem; ++l) same = split_alloc[l] == lateral_ksplit(l);
+    for (int l = 1; l < 4 && same && split_sem; ++l)
+      same = split_alloc[l] == lateral_ksplit(l) && split_tiling[l].tile_w == lat_tiling[l].tile_w;
     if (same) return;
     release_graphs();
     free_split();
     size_t sem_ints = 0, part_bytes = 0;
     size_t off[4] = {};
     for (int l = 1; l < 4; ++l) {
-      const ufpn::Conv3x3Tiling t = ufpn::default_tiling(H[l], W[l]);
+      const ufpn::Conv3x3Tiling t = lat_tiling[l];
       split_sem_off[l] = static_cast<int>(sem_ints);
       sem_ints += static_cast<size_t>(ufpn::neck_lateral_tiles(batch, H[l], W[l], t));
       off[l] = part_bytes;
@@ -256,6 +341,7 @@ struct UnifiedFPNCore::Impl {
     split_sem = static_cast<int*>(p);
     for (int l = 1; l < 4; ++l) {
       split_alloc[l] = lateral_ksplit(l);
+      split_tiling[l] = lat_tiling[l];
       split_part[l] = split_alloc[l] > 1
                           ? reinterpret_cast<float*>(static_cast<char*>(p) + sem_bytes + off[l])
                           : nullptr;
@@ -449,7 +535,7 @@ struct UnifiedFPNCore::Impl {
         lv[l].Cin = cin[l];
         lv[l].H = H[l];
         lv[l].W = W[l];
-        lv[l].lat_tiling = ufpn::default_tiling(H[l], W[l]);
+        lv[l].lat_tiling = lat_tiling[l];
         lv[l].conv_tiling = tiling_for(l);
         lv[l].act = act();
         lv[l].act_alpha = cfg.activation_alpha;
@@ -508,7 +594,7 @@ struct UnifiedFPNCore::Impl {
       lv[l].Cin = cin[l];
       lv[l].H = H[l];
       lv[l].W = W[l];
-      lv[l].lat_tiling = ufpn::default_tiling(H[l], W[l]);
+      lv[l].lat_tiling = lat_tiling[l];
       lv[l].conv_tiling = tiling_for(l);
       lv[l].act = act();
       lv[l].act_alpha = cfg.activation_alpha;
@@ -574,7 +660,7 @@ struct UnifiedFPNCore::Impl {
       for (int l = 2; l >= 1; --l) {
         ok(ufpn::launch_upsample_add(dtype, merged[l + 1], merged[l], merged[l], batch, cout,
                                      H[l + 1], W[l + 1], H[l], W[l], 0, Layout::NHWC, main,
-                                     nullptr, nullptr, chain),
+                                     nullptr, nullptr, chain, merge_units),
            "merge");
         if (prof_events) prof_record(3 + 2 * (2 - l), main);
         conv_level(l);
@@ -582,11 +668,22 @@ struct UnifiedFPNCore::Impl {
       }
     }
     TcPlan lat2;
-    check(ufpn::plan_tc_lateral(lat2, dtype, x[0], lat_wp[0], lat_b[0], merged[1], merged[0],
-                                batch, cin[0], H[0], W[0], H[1], W[1], lv[0].lat_tiling, d_status,
-                                0),
-          "plan lateral");
-    ufpn::tc_attach_wb_table(lat2, wb_table);
+    // p2_pair: CTA pairs with resident weight halves and fp32 top-down taps (when the level
+    // qualifies: Cin <= 256, taps within a 64-pixel box); else one CTA per tile with the
+    // top-down add as a tensor-core k-block.
+    const cudaError_t pe =
+        p2_pair ? ufpn::plan_tc_lateral_pair(lat2, dtype, x[0], lat_wp[0], lat_b[0], merged[1],
+                                             merged[0], batch, cin[0], H[0], W[0], H[1], W[1],
+                                             lv[0].lat_tiling, d_status, 0)
+                : cudaErrorNotSupported;
+    if (pe != cudaSuccess) {
+      if (pe != cudaErrorNotSupported) check(pe, "plan lateral pair");
+      check(ufpn::plan_tc_lateral(lat2, dtype, x[0], lat_wp[0], lat_b[0], merged[1], merged[0],
+                                  batch, cin[0], H[0], W[0], H[1], W[1], lv[0].lat_tiling,
+                                  d_status, 0),
+            "plan lateral");
+      ufpn::tc_attach_wb_table(lat2, wb_table);
+    }
     ok(ufpn::launch_tc(lat2, main, chain), "lateral launch");
     if (prof_events) prof_record(7, main);
     conv_level(0);
@@ -675,7 +772,7 @@ struct UnifiedFPNCore::Impl {
       void* lout = out_mode == 2 ? qmerged[l] : (l == 2 && two_level) ? lat4_raw : merged[l];
       check(ufpn::plan_tc_lateral(p, DType::E4M3, in[l], lat_wp[l], lat_b[l], coarse, lout,
                                   batch, cin[l], H[l], W[l], coarse ? H[l + 1] : 0,
-                                  coarse ? W[l + 1] : 0, ufpn::default_tiling(H[l], W[l]),
+                                  coarse ? W[l + 1] : 0, lat_tiling[l],
                                   d_status, 0, sc),
             "plan e4m3 lateral");
       if (l == 0) ufpn::tc_attach_wb_table(p, wb_table);
@@ -756,7 +853,8 @@ struct UnifiedFPNCore::Impl {
         if (!one_stream) check(cudaStreamWaitEvent(main, ev_lat_done[2 - l], 0), "event");
         ok(ufpn::launch_upsample_add(DType::BF16, merged[l + 1], merged[l], merged[l], batch,
                                      cout, H[l + 1], W[l + 1], H[l], W[l], 0, Layout::NHWC, main,
-                                     fp8_amax + l * batch, l == 1 ? &m3s : nullptr, opts(pdl)),
+                                     fp8_amax + l * batch, l == 1 ? &m3s : nullptr, opts(pdl),
+                                     merge_units),
            "merge");
         if (prof_events) prof_record(3 + 2 * (2 - l), main);
         conv_level(l);
@@ -877,7 +975,14 @@ void UnifiedFPNCore::configure_levels(const std::vector<FPNDimensions>& dims, in
       m.tiling[l] = tiling_from_code(it->second.first);
       m.tiling_tuned[l] = true;
     }
+    // lateral tiles: the standalone lateral tuner's choice for this shape, else the tiling
+    // with the fewest padded pixels
+    if (!ufpn::lateral_tiling_for(dt, N, m.cin[l], m.H[l], m.W[l], &m.lat_tiling[l]))
+      m.lat_tiling[l] = ufpn::default_tiling(m.H[l], m.W[l]);
   }
+  m.p2_pair = false;
+  m.merge_units = 0;
+  m.apply_tuning_db2();  // a whole-neck tuning of this geometry, if any
   const size_t esz = ufpn::dtype_size(dt);
   const size_t msz = dt == DType::E4M3 ? 2 : esz;  // merged maps: bf16 for e4m3 inputs
   size_t total = 0;
@@ -901,19 +1006,7 @@ void UnifiedFPNCore::configure_levels(const std::vector<FPNDimensions>& dims, in
     m.check(cudaMalloc(&m.lat4_raw, px4 * m.cout * msz), "workspace");
     total += px4 * m.cout * msz;
   }
-  if (m.tensor_core_path()) {
-    // The P2 lateral's top-down weights depend only on the geometry: build them once.
-    const Conv3x3Tiling lt = ufpn::default_tiling(m.H[0], m.W[0]);
-    const size_t tb = ufpn::tc_wb_table_bytes(m.H[0], m.W[0], m.H[1], m.W[1], lt);
-    if (tb > 0) {
-      m.check(cudaMalloc(&m.wb_table, tb), "workspace");
-      m.check(ufpn::tc_build_wb_table(dt, m.H[0], m.W[0], m.H[1], m.W[1], lt, m.wb_table,
-                                      m.setup),
-              "build bilinear weight table");
-      m.check(cudaStreamSynchronize(m.setup), "build bilinear weight table");
-      total += tb;
-    }
-  }
+
   if (dt == DType::E4M3) {
     const size_t words = 4 * static_cast<size_t>(N);
     m.check(cudaMalloc(&m.fp8_amax, 2 * words * sizeof(float)), "workspace");
@@ -930,6 +1023,7 @@ void UnifiedFPNCore::configure_levels(const std::vector<FPNDimensions>& dims, in
   }
   m.workspace_bytes = total;
   m.configured = true;
+  m.build_wb_table();
   if (m.weights_allocated) {
     m.packed_dtype = DType::F32;  // force repack in the new dtype
     m.ensure_weight_packing();
@@ -1014,7 +1108,7 @@ void UnifiedFPNCore::forward_raw_scaled(const void* const* in, const float* cons
   }
   DeviceGuard g(m.device);
   m.ensure_weight_packing();
-  m.ensure_split_workspace();
+  m.ensure_plan_buffers();
   if (m.profiling) {
     // The serialised schedule with an event between stages, captured and replayed as one
     // graph: the host's planning (tensor-map encoding) happens at capture, so the stage
@@ -1222,16 +1316,114 @@ int UnifiedFPNCore::device_status(bool reset) {
     if (impl_->split_sem) {
       size_t n = 0;
       for (int l = 1; l < 4; ++l)
-        n += static_cast<size_t>(ufpn::neck_lateral_tiles(
-            impl_->batch, impl_->H[l], impl_->W[l], ufpn::default_tiling(impl_->H[l], impl_->W[l])));
+        n += static_cast<size_t>(ufpn::neck_lateral_tiles(impl_->batch, impl_->H[l], impl_->W[l],
+                                                          impl_->split_tiling[l]));
       CUDA_CHECK(cudaMemset(impl_->split_sem, 0, n * sizeof(int)));
     }
   }
   return v;
 }
 
+// ------------------------------------------------------------------ named options
+namespace {
+struct EngineOption {
+  const char* name;
+  std::function<bool(int)> valid;
+  std::function<void(UnifiedFPNCore::Impl&, int)> set;
+  std::function<int(const UnifiedFPNCore::Impl&)> get;
+};
+bool in01(int v) { return v == 0 || v == 1; }
+bool lat_w_ok(int v) { return v == 8 || v == 16 || v == 32 || v == 64 || v == 128; }
+bool conv_code_ok(int v) { return v == -1 || v == 0 || lat_w_ok(v); }
+Conv3x3Tiling lat_from_w(int w) {
+  Conv3x3Tiling t;
+  t.tile_w = w;
+  t.tile_h = 128 / w;
+  return t;
+}
+template <bool FPNKernelConfig::*F>
+EngineOption bool_option(const char* name) {
+  return {name, in01, [](UnifiedFPNCore::Impl& m, int v) { m.cfg.*F = v != 0; },
+          [](const UnifiedFPNCore::Impl& m) { return (m.cfg.*F) ? 1 : 0; }};
+}
+const std::vector<EngineOption>& engine_options() {
+  static const std::vector<EngineOption> opts = [] {
+    std::vector<EngineOption> o;
+    o.push_back(bool_option<&FPNKernelConfig::grouped_topdown>("grouped_topdown"));
+    o.push_back(bool_option<&FPNKernelConfig::programmatic_launch>("programmatic_launch"));
+    o.push_back(bool_option<&FPNKernelConfig::chain_priority>("chain_priority"));
+    o.push_back(bool_option<&FPNKernelConfig::merge_two_levels>("merge_two_levels"));
+    o.push_back(bool_option<&FPNKernelConfig::single_stream>("single_stream"));
+    o.push_back(bool_option<&FPNKernelConfig::fused_neck_kernel>("fused_neck_kernel"));
+    o.push_back(bool_option<&FPNKernelConfig::fp8_two_pass_p2>("fp8_two_pass_p2"));
+    for (int l = 1; l < 4; ++l) {
+      static const char* names[4] = {"", "ksplit_p3", "ksplit_p4", "ksplit_p5"};
+      o.push_back({names[l], [](int v) { return v == 1 || v == 2 || v == 4; },
+                   [l](UnifiedFPNCore::Impl& m, int v) { m.cfg.lateral_ksplit[l] = v; },
+                   [l](const UnifiedFPNCore::Impl& m) { return m.cfg.lateral_ksplit[l]; }});
+    }
+    for (int l = 0; l < 4; ++l) {
+      static const char* lat[4] = {"lateral_tile_p2", "lateral_tile_p3", "lateral_tile_p4",
+                                   "lateral_tile_p5"};
+      static const char* conv[4] = {"conv3x3_p2", "conv3x3_p3", "conv3x3_p4", "conv3x3_p5"};
+      o.push_back({lat[l], lat_w_ok,
+                   [l](UnifiedFPNCore::Impl& m, int v) { m.lat_tiling[l] = lat_from_w(v); },
+                   [l](const UnifiedFPNCore::Impl& m) { return m.lat_tiling[l].tile_w; }});
+      o.push_back({conv[l], conv_code_ok,
+                   [l](UnifiedFPNCore::Impl& m, int v) {
+                     m.tiling[l] = tiling_from_code(v);
+                     m.tiling_tuned[l] = true;
+                   },
+                   [l](const UnifiedFPNCore::Impl& m) { return tiling_code(m.tiling[l]); }});
+    }
+    o.push_back({"p2_lateral_pair", in01,
+                 [](UnifiedFPNCore::Impl& m, int v) { m.p2_pair = v != 0; },
+                 [](const UnifiedFPNCore::Impl& m) { return m.p2_pair ? 1 : 0; }});
+    o.push_back({"merge_units", [](int v) { return v >= 0 && v <= 256; },
+                 [](UnifiedFPNCore::Impl& m, int v) { m.merge_units = v; },
+                 [](const UnifiedFPNCore::Impl& m) { return m.merge_units; }});
+    o.push_back({"test_stall_dependency_us", [](int v) { return v >= 0 && v <= 1000000; },
+                 [](UnifiedFPNCore::Impl& m, int v) { m.cfg.test_stall_dependency_us = v; },
+                 [](const UnifiedFPNCore::Impl& m) { return m.cfg.test_stall_dependency_us; }});
+    return o;
+  }();
+  return opts;
+}
+const EngineOption* find_option(const std::string& name) {
+  for (const auto& o : engine_options())
+    if (name == o.name) return &o;
+  return nullptr;
+}
+}  // namespace
+
+void UnifiedFPNCore::Impl::apply_tuning_db2() {
+  auto it = tuning_db2.find(geometry_key());
+  if (it == tuning_db2.end()) return;
+  for (const auto& kv : it->second.first) {
+    const EngineOption* o = find_option(kv.first);
+    if (o && o->valid(kv.second)) o->set(*this, kv.second);
+  }
+}
+
+void UnifiedFPNCore::set_option(const std::string& name, int value) {
+  const EngineOption* o = find_option(name);
+  if (!o) FPN_THROW("unknown option " + name);
+  if (!o->valid(value)) FPN_THROW("bad value for " + name + ": " + std::to_string(value));
+  DeviceGuard g(impl_->device);
+  impl_->release_graphs();
+  o->set(*impl_, value);
+}
+
+int UnifiedFPNCore::get_option(const std::string& name) const {
+  const EngineOption* o = find_option(name);
+  if (!o) FPN_THROW("unknown option " + name);
+  return o->get(*impl_);
+}
+
+// ------------------------------------------------------------------ autotuner
 std::string UnifiedFPNCore::autotune(const void* const* in, void* const* out, void* p6,
-                                     cudaStream_t stream, int iterations) {
+                                     cudaStream_t stream, int iterations,
+                                     const float* const* scales) {
   Impl& m = *impl_;
   if (!m.configured) FPN_THROW("configure_levels() has not been called");
   std::ostringstream rep;
@@ -1239,64 +1431,120 @@ std::string UnifiedFPNCore::autotune(const void* const* in, void* const* out, vo
     rep << "fp32 path: nothing to tune\n";
     return rep.str();
   }
-  if (m.dtype == DType::E4M3) {
-    rep << "e4m3 path: the 3x3 always uses 8 x 16 halo tiles on CTA pairs; nothing to tune\n";
-    return rep.str();
-  }
-  DeviceGuard g(m.device);
-  // One plain forward so the merged maps hold real data.
-  const bool saved_graph = m.cfg.enable_graph_capture;
-  m.cfg.enable_graph_capture = false;
-  forward_raw(in, out, p6, stream);
-  m.cfg.enable_graph_capture = saved_graph;
-  CUDA_CHECK(cudaStreamSynchronize(stream));
+  if (m.dtype == DType::E4M3 && !scales) FPN_THROW("FP8_E4M3 autotuning needs the input scales");
   if (iterations < 1) iterations = 1;
-  for (int l = 3; l >= 0; --l) {
-    float best_ms = -1.f;
-    int best_tw = tiling_code(m.tiling[l]);
-    for (int tw : {-1, 0, 8, 16, 32, 64, 128}) {  // -1 / 0 = halo tiles on CTA pairs / single
-      if (tw > 2 * m.W[l] && tw != 8) continue;  // wider than the image: pure padding
-      const Conv3x3Tiling t = tiling_from_code(tw);
-      TcPlan conv;
-      const bool nchw = m.layout == Layout::NCHW;
-      void* o = nchw ? m.nhwc_out[l] : out[l];
-      if (ufpn::plan_tc_conv3x3(conv, m.dtype, m.merged[l], m.out_wp[l], m.out_b[l], o, nullptr,
-                                m.batch, m.H[l], m.W[l], t, m.d_status, 0) != cudaSuccess)
-        continue;
-      CUDA_CHECK(ufpn::launch_tc(conv, stream));  // warm-up
-      CUDA_CHECK(cudaEventRecord(m.prof[0], stream));
-      for (int i = 0; i < iterations; ++i) CUDA_CHECK(ufpn::launch_tc(conv, stream));
-      CUDA_CHECK(cudaEventRecord(m.prof[1], stream));
-      CUDA_CHECK(cudaEventSynchronize(m.prof[1]));
+  DeviceGuard g(m.device);
+  const bool fp8 = m.dtype == DType::E4M3;
+  const bool saved_graph = m.cfg.enable_graph_capture;
+  m.cfg.enable_graph_capture = true;
+  cudaEvent_t e0 = m.prof[0], e1 = m.prof[1];
+  // One candidate: the whole forward, captured (second use of the pointer set) and replayed
+  // `iterations` times, three rounds; the fastest round.
+  auto measure = [&]() -> float {
+    m.release_graphs();
+    for (int i = 0; i < 2; ++i) forward_raw_scaled(in, scales, out, p6, stream);
+    float best = -1.f;
+    for (int r = 0; r < 3; ++r) {
+      CUDA_CHECK(cudaEventRecord(e0, stream));
+      for (int i = 0; i < iterations; ++i) forward_raw_scaled(in, scales, out, p6, stream);
+      CUDA_CHECK(cudaEventRecord(e1, stream));
+      CUDA_CHECK(cudaEventSynchronize(e1));
       float ms = 0.f;
-      cudaEventElapsedTime(&ms, m.prof[0], m.prof[1]);
-      ms /= iterations;
-      rep << "P" << (l + 2) << " 3x3 " << m.batch << "x" << m.H[l] << "x" << m.W[l] << " tile "
-          << t.tile_w << "x" << t.tile_h << (t.halo ? " halo" : "") << (t.pair ? " pair" : "")
-          << ": " << ms * 1e3
-          << " us\n";
-      if (best_ms < 0 || ms < best_ms) {
-        best_ms = ms;
-        best_tw = tw;
+      CUDA_CHECK(cudaEventElapsedTime(&ms, e0, e1));
+      ms /= static_cast<float>(iterations);
+      if (best < 0 || ms < best) best = ms;
+    }
+    if (device_status(true) != 0) FPN_THROW("device pipeline timeout during autotuning");
+    return best;
+  };
+  // Knobs and their candidates, in tuning order.
+  struct Knob {
+    std::string name;
+    std::vector<int> values;
+  };
+  std::vector<Knob> knobs;
+  for (int l = 0; l < 4; ++l) {
+    Knob k{"conv3x3_p" + std::to_string(l + 2), {}};
+    for (int v : fp8 ? std::vector<int>{-1, 0} : std::vector<int>{-1, 0, 8, 16, 32, 64, 128})
+      if (v <= 0 || v <= 2 * m.W[l] || v == 8) k.values.push_back(v);
+    knobs.push_back(k);
+  }
+  for (int l = 0; l < 4; ++l) {
+    Knob k{"lateral_tile_p" + std::to_string(l + 2), {}};
+    for (int v : {8, 16, 32, 64, 128})
+      if (v <= 2 * m.W[l] || v == 8) k.values.push_back(v);
+    knobs.push_back(k);
+  }
+  if (!fp8) {
+    if (m.cin[0] <= 256) knobs.push_back({"p2_lateral_pair", {0, 1}});
+    knobs.push_back({"grouped_topdown", {0, 1}});
+    knobs.push_back({"ksplit_p5", {1, 2, 4}});
+    knobs.push_back({"ksplit_p4", {1, 2, 4}});
+    knobs.push_back({"ksplit_p3", {1, 2}});
+    knobs.push_back({"programmatic_launch", {1, 0}});
+  } else {
+    knobs.push_back({"fp8_two_pass_p2", {0, 1}});
+  }
+  knobs.push_back({"merge_units", {0, 2, 4, 8, 16}});
+  knobs.push_back({"merge_two_levels", {0, 1}});
+  float best_all = measure();
+  rep << "start: " << best_all * 1e3 << " us per forward\n";
+  for (const auto& k : knobs) {
+    const EngineOption* o = find_option(k.name);
+    if (!o) continue;
+    const int start = o->get(m);
+    int best_v = start;
+    rep << k.name << ":";
+    for (int v : k.values) {
+      float ms;
+      if (v == start) {
+        ms = best_all;
+      } else {
+        o->set(m, v);
+        try {
+          m.ensure_plan_buffers();
+          ms = measure();
+        } catch (const FPNException&) {
+          ms = -1.f;  // a candidate this geometry cannot run (e.g. a plan limit): skipped
+          device_status(true);
+        }
+      }
+      rep << " " << v << "=" << (ms < 0 ? std::string("n/a") : std::to_string(ms * 1e3).substr(0, 6));
+      if (ms > 0 && ms < best_all) {
+        best_all = ms;
+        best_v = v;
       }
     }
-    m.tiling[l] = tiling_from_code(best_tw);
-    m.tiling_tuned[l] = true;
-    m.tuning_db[m.tuning_key(l)] = {best_tw, best_ms};
-    rep << "P" << (l + 2) << " -> tile " << m.tiling[l].tile_w << "x" << m.tiling[l].tile_h
-        << (m.tiling[l].halo ? " halo" : "") << (m.tiling[l].pair ? " pair" : "") << "\n";
+    o->set(m, best_v);
+    m.ensure_plan_buffers();
+    rep << " -> " << best_v << "\n";
   }
+  // Record every knob of this geometry (save_tuning persists them; configuring the same
+  // geometry again applies them).
+  std::map<std::string, int> chosen;
+  for (const auto& k : knobs) {
+    const EngineOption* o = find_option(k.name);
+    if (o) chosen[k.name] = o->get(m);
+  }
+  m.tuning_db2[m.geometry_key()] = {chosen, best_all};
+  for (int l = 0; l < 4; ++l) m.tuning_db[m.tuning_key(l)] = {tiling_code(m.tiling[l]), best_all};
+  m.cfg.enable_graph_capture = saved_graph;
   m.release_graphs();
-  if (device_status(true) != 0) FPN_THROW("device pipeline timeout during autotuning");
+  rep << "tuned: " << best_all * 1e3 << " us per forward (" << m.geometry_key() << ")\n";
   return rep.str();
 }
 
 bool UnifiedFPNCore::save_tuning(const std::string& path) const {
   std::ofstream f(path);
   if (!f) return false;
-  f << "ufpn-tuning 1\n";
+  f << "ufpn-tuning 2\n";
+  for (auto& kv : impl_->tuning_db2) {
+    f << "neck " << kv.first << " " << kv.second.second;
+    for (auto& o : kv.second.first) f << " " << o.first << "=" << o.second;
+    f << "\n";
+  }
   for (auto& kv : impl_->tuning_db)
-    f << kv.first << " " << kv.second.first << " " << kv.second.second << "\n";
+    f << "conv3x3 " << kv.first << " " << kv.second.first << " " << kv.second.second << "\n";
   return static_cast<bool>(f);
 }
 
@@ -1306,15 +1554,41 @@ bool UnifiedFPNCore::load_tuning(const std::string& path) {
   std::string magic;
   int ver = 0;
   f >> magic >> ver;
-  if (magic != "ufpn-tuning" || ver != 1) return false;
-  std::string key;
-  int tw;
-  float ms;
-  while (f >> key >> tw >> ms) {
-    if (tw == -1 || tw == 0 || (tw >= 8 && tw <= 128 && 128 % tw == 0))
-      impl_->tuning_db[key] = {tw, ms};
-  }
+  if (magic != "ufpn-tuning" || (ver != 1 && ver != 2)) return false;
   Impl& m = *impl_;
+  std::string line;
+  std::getline(f, line);
+  while (std::getline(f, line)) {
+    std::istringstream ls(line);
+    if (ver == 1) {  // key tile_w ms
+      std::string key;
+      int tw;
+      float ms;
+      if ((ls >> key >> tw >> ms) && (tw == -1 || tw == 0 || lat_w_ok(tw))) m.tuning_db[key] = {tw, ms};
+      continue;
+    }
+    std::string kind, key;
+    if (!(ls >> kind >> key)) continue;
+    if (kind == "conv3x3") {
+      int tw;
+      float ms;
+      if ((ls >> tw >> ms) && conv_code_ok(tw)) m.tuning_db[key] = {tw, ms};
+    } else if (kind == "neck") {
+      float ms;
+      if (!(ls >> ms)) continue;
+      std::map<std::string, int> knobs;
+      std::string kv;
+      while (ls >> kv) {
+        const size_t eq = kv.find('=');
+        if (eq == std::string::npos) continue;
+        const std::string name = kv.substr(0, eq);
+        const EngineOption* o = find_option(name);
+        const int v = std::atoi(kv.c_str() + eq + 1);
+        if (o && o->valid(v)) knobs[name] = v;
+      }
+      m.tuning_db2[key] = {knobs, ms};
+    }
+  }
   if (m.configured) {
     for (int l = 0; l < 4; ++l) {
       auto it = m.tuning_db.find(m.tuning_key(l));
@@ -1323,6 +1597,7 @@ bool UnifiedFPNCore::load_tuning(const std::string& path) {
         m.tiling_tuned[l] = true;
       }
     }
+    m.apply_tuning_db2();
     m.release_graphs();
   }
   return true;

@@ -896,7 +896,8 @@ cudaError_t absmax_t(const void* x, long long n, int groups, unsigned* amax, cud
 template <typename T>
 cudaError_t upsample_add_t(const void* coarse, const void* lat, void* out, int N, int C, int Hc,
                            int Wc, int H, int W, int ac, Layout layout, cudaStream_t s,
-                           unsigned* amax, const MergeScaledCopy* sc, LaunchOpts opts) {
+                           unsigned* amax, const MergeScaledCopy* sc, LaunchOpts opts,
+                           int units_per_block) {
   const float sy = (ac && H > 1) ? static_cast<float>(Hc - 1) / (H - 1)
                                  : static_cast<float>(Hc) / H;
   const float sx = (ac && W > 1) ? static_cast<float>(Wc - 1) / (W - 1)
@@ -928,7 +929,7 @@ cudaError_t upsample_add_t(const void* coarse, const void* lat, void* out, int N
         }
         const long long g = units < res ? units : res;
         if (g <= 0) return cudaSuccess;
-        const long long per = (units + g - 1) / g;
+        const long long per = units_per_block > 0 ? units_per_block : (units + g - 1) / g;
         if (per >= (1LL << 31)) return cudaErrorInvalidValue;
         const int grid = static_cast<int>((units + per - 1) / per);
         return launch_ex(kern, dim3(grid), dim3(256), 0, s, opts, 1, c, l, o, N, Hc, Wc, H, W,
@@ -1002,20 +1003,22 @@ cudaError_t transpose_t(const void* in, void* out, int N, int C, int HW, bool to
 cudaError_t launch_upsample_add(DType dt, const void* coarse, const void* lat, void* out, int N,
                                 int C, int Hc, int Wc, int H, int W, int align_corners,
                                 Layout layout, cudaStream_t s, unsigned* amax_out,
-                                const MergeScaledCopy* scaled, LaunchOpts opts) {
+                                const MergeScaledCopy* scaled, LaunchOpts opts,
+                                int units_per_block) {
   if (scaled && (!scaled->out || !scaled->scale_a || !scaled->scale_w || !aligned16(scaled->out)))
     return cudaErrorInvalidValue;
+  if (units_per_block < 0) return cudaErrorInvalidValue;
   switch (dt) {
     case DType::F32:
       if (scaled) return cudaErrorNotSupported;
       return upsample_add_t<float>(coarse, lat, out, N, C, Hc, Wc, H, W, align_corners, layout, s,
-                                   amax_out, nullptr, opts);
+                                   amax_out, nullptr, opts, units_per_block);
     case DType::F16:
       return upsample_add_t<__half>(coarse, lat, out, N, C, Hc, Wc, H, W, align_corners, layout,
-                                    s, amax_out, scaled, opts);
+                                    s, amax_out, scaled, opts, units_per_block);
     case DType::BF16:
       return upsample_add_t<__nv_bfloat16>(coarse, lat, out, N, C, Hc, Wc, H, W, align_corners,
-                                           layout, s, amax_out, scaled, opts);
+                                           layout, s, amax_out, scaled, opts, units_per_block);
     default:
       return cudaErrorInvalidValue;
   }

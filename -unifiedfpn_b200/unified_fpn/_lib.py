@@ -163,6 +163,8 @@ SIGNATURES = {
     "print_upsample_profiling_summary": (None, [c_void_p]),
     "export_upsample_profiling_data": (c_int, [c_void_p, c_char_p]),
     "fpn_auto_tune_lateral_conv": (POINTER(TuningResult), [c_int, c_int, c_int, c_int, c_int]),
+    "ufpn_autotune_lateral": (c_int, [c_int, c_int, c_int, c_int, c_int, c_void_p, POINTER(TuningResult)]),
+    "ufpn_core_autotune_scaled": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int]),
     "fpn_auto_tune_save_results": (None, [c_char_p]),
 }
 

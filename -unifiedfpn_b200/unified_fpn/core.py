@@ -332,9 +332,11 @@ class UnifiedFPN:
         check(lib.ufpn_core_set_fp8_options(self._h, int(fp8_two_pass_p2)), "set_fp8_options")
 
     def set_option(self, name: str, value: int) -> None:
-        """Named schedule option (``ufpn_core_set_option``): "grouped_topdown" (0/1),
-        "ksplit_p3" / "ksplit_p4" / "ksplit_p5" (1, 2 or 4 units per lateral tile over K in
-        the grouped lateral launch), and the switches of :meth:`set_schedule`."""
+        """Named option of the schedule or a per-level kernel shape (``ufpn_core_set_option``
+        lists them): "lateral_tile_p2".."lateral_tile_p5" (8..128), "conv3x3_p2".."conv3x3_p5"
+        (-1 halo tiles on CTA pairs, 0 halo tiles, 8..128 plain tiles), "p2_lateral_pair",
+        "merge_units", "grouped_topdown", "ksplit_p3".."ksplit_p5" (1, 2 or 4), and the
+        switches of :meth:`set_schedule`."""
         check(lib.ufpn_core_set_option(self._h, name.encode(), int(value)), f"set_option({name})")
 
     def get_option(self, name: str) -> int:
@@ -365,13 +367,20 @@ class UnifiedFPN:
     def get_memory_usage(self) -> int:
         return int(lib.ufpn_core_get_memory_usage(self._h))
 
-    def autotune(self, backbone_features, iterations: int = 10) -> str:
-        """Times every candidate 3x3 tiling per level and keeps the fastest."""
+    def autotune(self, backbone_features, iterations: int = 10, input_scales=None) -> str:
+        """Tunes the schedule for these features' geometry: every knob of :meth:`set_option`
+        that applies (per level: 3x3 tiling, lateral tile shape; the P2 lateral on CTA pairs,
+        the grouped lateral launch's top-down adds and split-K, the merge grid, programmatic
+        launches, the two-level merge; e4m3: pair / single 3x3, the two-pass P2 lateral) is
+        set to each candidate in turn, each timed as the whole forward; the fastest values
+        are applied and kept for the geometry (save_tuning).  Returns the report.
+        float8_e4m3fn inputs need ``input_scales`` as for forward."""
         feats, layout, mf = self._prepare(backbone_features)
         outs, p6 = self._alloc_outputs(feats, mf, True)
-        check(lib.ufpn_core_autotune(self._h, _ptr_array([t.data_ptr() for t in feats]),
-                                     _ptr_array([t.data_ptr() for t in outs]), p6.data_ptr(),
-                                     _stream(feats[0]), iterations), "autotune")
+        sp = self._scale_ptrs(input_scales) if feats[0].dtype == E4M3 else None
+        check(lib.ufpn_core_autotune_scaled(self._h, _ptr_array([t.data_ptr() for t in feats]), sp,
+                                            _ptr_array([t.data_ptr() for t in outs]), p6.data_ptr(),
+                                            _stream(feats[0]), iterations), "autotune")
         return lib.ufpn_last_error().decode()
 
     def save_tuning(self, path: str) -> None:

@@ -56,21 +56,33 @@ class __attribute__((visibility("default"))) UnifiedFPNCore {
   FPNKernelConfig get_kernel_config() const;
   size_t get_memory_usage() const;
 
-  // Time every kernel of the next forward() with CUDA events (serialises the
-  // schedule; synchronises the stream at the end of that forward).
   // Graph cache counters: [0] pointer sets captured into a graph, [1] graph replays,
   // [2] forwards launched directly (a pointer set's first use), [3] graphs cached now.
   void graph_stats(long long* out4) const;
+  // Time every kernel of the next forward() with CUDA events (serialises the
+  // schedule; synchronises the stream at the end of that forward).
   void set_profiling(bool enable);
+  // Named integer options of the schedule and of the per-level kernel shapes (the knobs the
+  // autotuner sets; the C ABI's ufpn_core_set_option lists them).  Throws FPNException on an
+  // unknown name or value.
+  void set_option(const std::string& name, int value);
+  int get_option(const std::string& name) const;
   // Record the fused neck kernel's device timeline during the next forward() (launched
   // directly, then the stream is synchronised).  get_neck_trace returns globaltimer ns:
   // [0] start, [1..4] P2..P5 laterals complete, [5] end, [6] first P2 3x3 tile started.
   void trace_next_forward();
   void get_neck_trace(unsigned long long* out8) const;
-  // Measure the candidate tilings of every level with the given buffers and keep
-  // the fastest; returns a human-readable report.
+  // Tunes the schedule for the configured geometry with the given buffers: every knob
+  // (per level: 3x3 tiling, lateral tile shape; the P2 lateral on CTA pairs, the grouped
+  // lateral launch's top-down adds and split-K, the merge grid, programmatic launches, the
+  // two-level merge; e4m3: the 3x3 pair / single CTA, the two-pass P2 lateral) is set to each
+  // candidate in turn, each timed as the whole forward (graph replays on `stream`), keeping
+  // the fastest (coordinate descent).  The result is kept for this geometry (save_tuning /
+  // load_tuning) and applied; returns a human-readable report.  FP8_E4M3: input_scales as
+  // for forward_raw_scaled.
   std::string autotune(const void* const* inputs, void* const* outputs, void* p6,
-                       cudaStream_t stream, int iterations = 10);
+                       cudaStream_t stream, int iterations = 10,
+                       const float* const* input_scales = nullptr);
   bool save_tuning(const std::string& path) const;
   bool load_tuning(const std::string& path);
 

@@ -53,11 +53,13 @@ struct MergeScaledCopy {
 };
 // amax_out (optional): amax_out[n] = atomicMax of |out| of image n as fp32 bits (the caller
 // zeroes them first).  scaled (optional): also write the scaled copy.
+// units_per_block (NHWC, 256 channels of a 16-bit type): 8-pixel row units each block walks
+// (0: automatic -- one wave of the blocks resident at once, each with a contiguous run).
 cudaError_t launch_upsample_add(DType dt, const void* coarse, const void* lat, void* out, int N,
                                 int C, int Hc, int Wc, int H, int W, int align_corners,
                                 Layout layout, cudaStream_t s, unsigned* amax_out = nullptr,
                                 const MergeScaledCopy* scaled = nullptr,
-                                LaunchOpts opts = LaunchOpts());
+                                LaunchOpts opts = LaunchOpts(), int units_per_block = 0);
 // Two top-down merges in one launch (NHWC, 256 channels, bf16 / fp16, maps that upsample):
 // M4 = L4 + up(M5) into m4 and M3 = L3 + up(M4) in place (l3 may alias m3; l4 must not
 // alias m4).  Bitwise the same as launch_upsample_add for M4 then for M3 (the reference's

@@ -126,10 +126,22 @@ int ufpn_core_set_schedule(ufpn_core* core, int fused_neck_kernel);
 int ufpn_core_set_schedule_options(ufpn_core* core, int programmatic_launch, int chain_priority,
                                    int merge_two_levels);
 /* fpn_engine.cu:408-415 (get_memory_usage) */
-/* Named integer options of the schedule (no reference counterpart; the reference's
- * FPNKernelConfig had fixed fields, types.h:265-293).  Every option keeps the results within
- * the tolerances; each one's default is the measured faster choice at the R50 800x1216
- * batch-2 workload, and the autotuner (ufpn_core_autotune) may change them per geometry.
+/* Named integer options of the schedule and of the per-level kernel shapes (no reference
+ * counterpart; the reference's FPNKernelConfig had fixed fields, types.h:265-293).  Every
+ * option keeps the results within the tolerances; each default is the measured faster choice
+ * at the R50 800x1216 batch-2 workload, and the autotuner (ufpn_core_autotune) sets them per
+ * geometry.  Per level (p2..p5):
+ *   "lateral_tile_pN"   8/16/32/64/128  lateral tile width (height 128 / width); default the
+ *                            shape with the fewest padded pixels, or fpn_auto_tune_lateral_conv's
+ *   "conv3x3_pN"        -1/0/8..128  3x3 tiling: -1 8x16 halo tiles on CTA pairs, 0 halo tiles
+ *                            on single CTAs, 8..128 plain tiles of that width
+ * and for the whole neck:
+ *   "p2_lateral_pair"   0/1  16-bit P2 lateral on CTA pairs with resident weight halves and
+ *                            fp32 top-down taps (when Cin <= 256), else one CTA per tile with
+ *                            the top-down add as a tensor-core k-block
+ *   "merge_units"       0..256  8-pixel units per block of the top-down merge kernels (0:
+ *                            automatic, one wave of resident blocks)
+ *   "fp8_two_pass_p2"   0/1  as ufpn_core_set_fp8_options
  *   "grouped_topdown"   0/1  the grouped P5/P4/P3 lateral launch also does the top-down adds
  *                            of M4 and M3 (device-side level counters) instead of two merge
  *                            kernels after it (16-bit split schedule)
@@ -169,6 +181,14 @@ int ufpn_core_get_neck_trace(const ufpn_core* core, unsigned long long* out8);
 /* lib/utils/auto_tuner.cu:213-275 (auto_tune_lateral_conv), for every level of the neck. */
 int ufpn_core_autotune(ufpn_core* core, const void* const* inputs, void* const* outputs,
                        void* p6, void* stream, int iterations);
+/* ufpn_core_autotune for any input type: FP8_E4M3 inputs pass their per-tensor device scales
+ * (as ufpn_core_forward_e4m3); other types NULL.  Every knob of ufpn_core_set_option that
+ * applies to the geometry is tried in turn, each candidate timed as the whole forward on
+ * `stream`; the fastest values are applied, kept for the geometry (save / load_tuning) and
+ * reported (ufpn_last_error holds the report). */
+int ufpn_core_autotune_scaled(ufpn_core* core, const void* const* inputs,
+                              const float* const* input_scales, void* const* outputs, void* p6,
+                              void* stream, int iterations);
 /* auto_tuner.cu:305-323 (save_tuning_results) plus the missing load. */
 int ufpn_core_save_tuning(const ufpn_core* core, const char* path);
 int ufpn_core_load_tuning(ufpn_core* core, const char* path);
@@ -436,7 +456,7 @@ int export_upsample_profiling_data(void* engine, const char* filename);
 /* lib/utils/auto_tuner.cu:8-25: the reference's TuningResult carries a std::string;
  * this C-layout version carries a fixed buffer instead. */
 typedef struct {
-  int tile_w;              /* chosen 3x3 tile width (lateral: 0) */
+  int tile_w;              /* chosen lateral tile width (128-pixel tiles, height 128 / width) */
   int tile_h;
   int num_ctas;            /* persistent CTAs launched */
   float time_ms;           /* measured */
@@ -445,9 +465,16 @@ typedef struct {
   char architecture_name[32];
 } TuningResult;
 
-/* auto_tuner.cu:328-333: times the tensor-core lateral (bf16) on a synthetic problem of
- * this shape for every CTA-count candidate; out_channels must be 256.  Returns a pointer
- * to a per-shape cached result (valid until process exit), NULL on error. */
+/* Tunes the tensor-core lateral 1x1 (bf16 / fp16 dtype code) for one shape on seeded random
+ * data: every 128-pixel tile shape (width 8..128) timed on `stream`; the fastest goes to
+ * *out and into a process-wide table from which engines configuring a level of that shape
+ * (batch, Cin, H, W, dtype) take their lateral tile shape.  No reference counterpart
+ * (the stream-taking form of the entry point below). */
+int ufpn_autotune_lateral(int dtype, int batch_size, int in_channels, int height, int width,
+                          void* stream, TuningResult* out);
+/* auto_tuner.cu:328-333: ufpn_autotune_lateral for bf16 on the calling thread's default
+ * stream; out_channels must be 256.  Returns a pointer to a per-shape cached result (valid
+ * until process exit), NULL on error. */
 TuningResult* fpn_auto_tune_lateral_conv(int batch_size, int in_channels, int out_channels,
                                          int height, int width);
 /* auto_tuner.cu:335-338 */

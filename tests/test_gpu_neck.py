@@ -553,3 +553,85 @@ def test_graph_cache_with_fresh_outputs_every_call(cuda_device):
     assert st2["captures"] == 1 and st2["replays"] == 3 and st2["direct"] == 22, st2
     assert all(torch.equal(a, b) for a, b in zip(out, ref))
     assert fpn.device_status() == 0
+
+
+def test_autotune_moves_a_bad_lateral_choice_and_keeps_parity(cuda_device, tmp_path):
+    """Whole-neck tuning (every knob timed inside the full forward): started from 128-pixel-wide
+    P2 lateral tiles on a 40-pixel-wide map (3.2x padded work), the tuner picks another shape;
+    the tuned forward matches the oracle; save/load re-applies every tuned knob."""
+    import unified_fpn as U
+    sizes = O.level_sizes(1024, 160)  # P2 256 x 40 ... P5 32 x 5
+    host = O.make_features(1, O.R50_CHANNELS, sizes, seed=101)
+    wts = O.make_weights(O.R50_CHANNELS, seed=102, bias_scale=0.1)
+    xin = [_cl(f.to(torch.bfloat16).cuda()) for f in host]
+    fpn = U.UnifiedFPN()
+    fpn.initialize_weights(wts.lat_w, wts.lat_b, wts.out_w, wts.out_b)
+    _run(fpn, xin)
+    fpn.set_option("lateral_tile_p2", 128)
+    report = fpn.autotune(xin, iterations=3)
+    assert "lateral_tile_p2" in report and "tuned:" in report, report
+    assert fpn.get_option("lateral_tile_p2") != 128, report
+    outs = [o.clone() for o in _run(fpn, xin)]
+    assert fpn.device_status() == 0
+    rw = O.NeckWeights([O.round_to(w, torch.bfloat16) for w in wts.lat_w], wts.lat_b,
+                       [O.round_to(w, torch.bfloat16) for w in wts.out_w], wts.out_b)
+    _check(outs, O.fpn_neck([O.round_to(f, torch.bfloat16) for f in host], rw), torch.bfloat16)
+    names = [f"lateral_tile_p{l}" for l in range(2, 6)] + [f"conv3x3_p{l}" for l in range(2, 6)] + \
+            ["p2_lateral_pair", "grouped_topdown", "ksplit_p3", "ksplit_p4", "ksplit_p5", "merge_units",
+             "merge_two_levels", "programmatic_launch"]
+    tuned = {n: fpn.get_option(n) for n in names}
+    path = tmp_path / "tune.txt"
+    fpn.save_tuning(path)
+    fpn2 = U.UnifiedFPN()
+    fpn2.initialize_weights(wts.lat_w, wts.lat_b, wts.out_w, wts.out_b)
+    fpn2.load_tuning(path)
+    again = _run(fpn2, xin)  # configures this geometry: the saved knobs apply
+    assert {n: fpn2.get_option(n) for n in names} == tuned
+    assert all(torch.equal(a, b) for a, b in zip(outs, again))
+
+
+def test_autotune_e4m3_keeps_parity(cuda_device):
+    import numpy as np
+    import unified_fpn as U
+    chans, sizes = O.R50_CHANNELS, O.level_sizes(128, 192)
+    feats = O.make_features(2, chans, sizes, seed=111, dist="normal")
+    wts = O.make_weights(chans, seed=112, bias_scale=0.1)
+    qf, sc = zip(*[O.quantize_e4m3_tensor(f) for f in feats])
+    qf = [torch.from_numpy(q) for q in qf]
+    fpn = U.UnifiedFPN()
+    fpn.initialize_weights(wts.lat_w, wts.lat_b, wts.out_w, wts.out_b)
+    xin = [_cl(q.to(torch.float8_e4m3fn).cuda()) for q in qf]
+    scales = [float(s) for s in sc]
+    fpn(xin, return_p6=True, input_scales=scales)
+    report = fpn.autotune(xin, iterations=2, input_scales=scales)
+    assert "conv3x3_p2" in report and "fp8_two_pass_p2" in report, report
+    outs = fpn(xin, return_p6=True, input_scales=scales)
+    torch.cuda.synchronize()
+    assert fpn.device_status() == 0
+    ref = O.fpn_neck_e4m3(qf, [np.float32(s) for s in sc], O.quantize_neck_weights(wts))
+    for o, r in zip(outs, ref):
+        O.check_close(o.float().cpu(), r, "e4m3")
+
+
+def test_lateral_tuner_feeds_the_engine(cuda_device):
+    """fpn_auto_tune_lateral_conv (the reference's C entry point) tunes the lateral tile shape
+    of one shape; an engine configuring a level of that shape afterwards uses it."""
+    import unified_fpn as U
+    from unified_fpn import _lib
+    res = _lib.lib.fpn_auto_tune_lateral_conv(1, 512, 256, 160, 24)
+    assert res, _lib.lib.ufpn_last_error()
+    r = res.contents
+    assert r.tile_w in (8, 16, 32, 64, 128) and r.tile_h * r.tile_w == 128
+    assert r.time_ms > 0 and r.performance_gflops > 0
+    sizes = [(320, 48), (160, 24), (80, 12), (40, 6)]  # P3 level: 1 x 512 x 160 x 24
+    fpn = U.UnifiedFPN()
+    _run(fpn, [_cl(torch.randn(1, c, h, w, device="cuda", dtype=torch.bfloat16))
+               for c, (h, w) in zip(O.R50_CHANNELS, sizes)])
+    assert fpn.get_option("lateral_tile_p3") == r.tile_w
+    # the stream-taking form, fp16
+    out = _lib.TuningResult()
+    import ctypes
+    assert _lib.lib.ufpn_autotune_lateral(_lib.DTYPE_F16, 2, 256, 50, 76,
+                                          torch.cuda.current_stream().cuda_stream,
+                                          ctypes.byref(out)) == 0
+    assert out.tile_w in (8, 16, 32, 64, 128) and out.time_ms > 0
