@@ -1438,24 +1438,23 @@ std::string UnifiedFPNCore::autotune(const void* const* in, void* const* out, vo
   const bool saved_graph = m.cfg.enable_graph_capture;
   m.cfg.enable_graph_capture = true;
   cudaEvent_t e0 = m.prof[0], e1 = m.prof[1];
-  // One candidate: the whole forward, captured (second use of the pointer set) and replayed
-  // `iterations` times, three rounds; the fastest round.
+  // One sample of the current settings: the whole forward, captured (second use of the
+  // pointer set) and replayed `iterations` times; ms per forward.
   auto measure = [&]() -> float {
     m.release_graphs();
     for (int i = 0; i < 2; ++i) forward_raw_scaled(in, scales, out, p6, stream);
-    float best = -1.f;
-    for (int r = 0; r < 3; ++r) {
-      CUDA_CHECK(cudaEventRecord(e0, stream));
-      for (int i = 0; i < iterations; ++i) forward_raw_scaled(in, scales, out, p6, stream);
-      CUDA_CHECK(cudaEventRecord(e1, stream));
-      CUDA_CHECK(cudaEventSynchronize(e1));
-      float ms = 0.f;
-      CUDA_CHECK(cudaEventElapsedTime(&ms, e0, e1));
-      ms /= static_cast<float>(iterations);
-      if (best < 0 || ms < best) best = ms;
-    }
+    CUDA_CHECK(cudaEventRecord(e0, stream));
+    for (int i = 0; i < iterations; ++i) forward_raw_scaled(in, scales, out, p6, stream);
+    CUDA_CHECK(cudaEventRecord(e1, stream));
+    CUDA_CHECK(cudaEventSynchronize(e1));
+    float ms = 0.f;
+    CUDA_CHECK(cudaEventElapsedTime(&ms, e0, e1));
     if (device_status(true) != 0) FPN_THROW("device pipeline timeout during autotuning");
-    return best;
+    return ms / static_cast<float>(iterations);
+  };
+  auto median = [](std::vector<float> v) {
+    std::sort(v.begin(), v.end());
+    return v.empty() ? -1.f : v[v.size() / 2];
   };
   // Knobs and their candidates, in tuning order.
   struct Knob {
@@ -1487,38 +1486,49 @@ std::string UnifiedFPNCore::autotune(const void* const* in, void* const* out, vo
   }
   knobs.push_back({"merge_units", {0, 2, 4, 8, 16}});
   knobs.push_back({"merge_two_levels", {0, 1}});
-  float best_all = measure();
-  rep << "start: " << best_all * 1e3 << " us per forward\n";
+  // Each candidate is compared with the incumbent in back-to-back pairs (the GPU's clock,
+  // which drifts over seconds under a power cap, is the same within a pair); it replaces the
+  // incumbent if the median of its time ratios shows a gain of at least kMinGain.
+  constexpr int kPairs = 3;
+  constexpr float kMinGain = 0.02f;
+  float best_all = -1.f;
   for (const auto& k : knobs) {
     const EngineOption* o = find_option(k.name);
     if (!o) continue;
-    const int start = o->get(m);
-    int best_v = start;
-    rep << k.name << ":";
+    int inc = o->get(m);
+    rep << k.name << " (" << inc << "):";
     for (int v : k.values) {
-      float ms;
-      if (v == start) {
-        ms = best_all;
-      } else {
-        o->set(m, v);
-        try {
+      if (v == inc) continue;
+      std::vector<float> ratios;
+      float v_ms = -1.f;
+      try {
+        for (int r = 0; r < kPairs; ++r) {
+          o->set(m, inc);
           m.ensure_plan_buffers();
-          ms = measure();
-        } catch (const FPNException&) {
-          ms = -1.f;  // a candidate this geometry cannot run (e.g. a plan limit): skipped
-          device_status(true);
+          const float a = measure();
+          o->set(m, v);
+          m.ensure_plan_buffers();
+          const float b = measure();
+          ratios.push_back(b / a);
+          v_ms = b;
+          if (best_all < 0) best_all = a;
         }
+      } catch (const FPNException&) {
+        ratios.clear();  // a candidate this geometry cannot run (e.g. a plan limit)
+        device_status(true);
       }
-      rep << " " << v << "=" << (ms < 0 ? std::string("n/a") : std::to_string(ms * 1e3).substr(0, 6));
-      if (ms > 0 && ms < best_all) {
-        best_all = ms;
-        best_v = v;
+      const float q = median(ratios);
+      rep << " " << v << (q < 0 ? std::string("=n/a") : "=" + std::to_string(q).substr(0, 5) + "x");
+      if (q > 0 && q < 1.f - kMinGain) {
+        inc = v;
+        best_all = v_ms;
       }
     }
-    o->set(m, best_v);
+    o->set(m, inc);
     m.ensure_plan_buffers();
-    rep << " -> " << best_v << "\n";
+    rep << " -> " << inc << "\n";
   }
+  if (best_all < 0) best_all = measure();
   // Record every knob of this geometry (save_tuning persists them; configuring the same
   // geometry again applies them).
   std::map<std::string, int> chosen;

@@ -555,6 +555,51 @@ __global__ void __launch_bounds__(256) upsample_add_nchw_kernel(
   }
 }
 
+// Vectorised NCHW upsample-add (W % 8 == 0, 16-byte aligned rows of a 16-bit type): a thread
+// makes 8 consecutive outputs of one row -- one 16-byte lateral load and store, the row's
+// source coordinate and its two coarse rows computed once per 8 outputs -- with the
+// arithmetic of upsample_add_nchw_kernel element for element.  The scalar kernel did two
+// 64-bit divisions per element and ran at 0.14 of HBM bandwidth on a 4x256x400x608 map.
+template <typename T>
+__global__ void __launch_bounds__(256) upsample_add_nchw_vec_kernel(
+    const T* __restrict__ coarse, const T* __restrict__ lat, T* __restrict__ out, int N, int C,
+    int Hc, int Wc, int H, int W, float sy_scale, float sx_scale, int ac) {
+  static_assert(sizeof(T) == 2, "16-bit types");
+  griddep_wait();  // (programmatic launch) inputs written by the previous kernel
+  griddep_launch_dependents();
+  const int vpr = W >> 3;  // 8-element vectors per row
+  const long long total = static_cast<long long>(N) * C * H * vpr;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long row = i / vpr;
+    const int x0v = static_cast<int>(i - row * vpr) * 8;
+    const long long plane = row / H;
+    const int y = static_cast<int>(row - plane * H);
+    const float sy = src_coord(y, Hc, H, sy_scale, ac);
+    const int ya = static_cast<int>(sy);
+    const int yb = min(ya + 1, Hc - 1);
+    const float wy = sy - static_cast<float>(ya);
+    const T* c0 = coarse + (static_cast<size_t>(plane) * Hc + ya) * Wc;
+    const T* c1 = coarse + (static_cast<size_t>(plane) * Hc + yb) * Wc;
+    const size_t o = static_cast<size_t>(row) * W + x0v;
+    Vec16<T> l, r;
+    if (lat) l.u = __ldg(reinterpret_cast<const uint4*>(lat + o));
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float sx = src_coord(x0v + e, Wc, W, sx_scale, ac);
+      const int xa = static_cast<int>(sx);
+      const int xb = min(xa + 1, Wc - 1);
+      const float wx = sx - static_cast<float>(xa);
+      float v = to_f(__ldg(c0 + xa)) * ((1.f - wy) * (1.f - wx)) +
+                to_f(__ldg(c0 + xb)) * ((1.f - wy) * wx) +
+                to_f(__ldg(c1 + xa)) * (wy * (1.f - wx)) + to_f(__ldg(c1 + xb)) * (wy * wx);
+      if (lat) v += to_f(l.e[e]);
+      r.e[e] = from_f<T>(v);
+    }
+    *reinterpret_cast<uint4*>(out + o) = r.u;
+  }
+}
+
 // ---------------------------------------------------------------- P6
 // P6 = max_pool2d(P5, kernel=1, stride=2): a single-element window, i.e. P5[::2, ::2].
 template <typename T, bool kVec>
@@ -583,6 +628,34 @@ __global__ void __launch_bounds__(256) p6_nhwc_kernel(const T* __restrict__ in,
         }
       }
     }
+  }
+}
+
+// NCHW with W % 16 == 0 (16-bit, 16-byte aligned rows): a thread makes 8 outputs of one row
+// from two 16-byte loads of the even input row (the even elements kept), one 16-byte store.
+template <typename T>
+__global__ void __launch_bounds__(256) p6_nchw_vec_kernel(const T* __restrict__ in,
+                                                          T* __restrict__ out, int N, int C,
+                                                          int H, int W, int H6, int W6) {
+  static_assert(sizeof(T) == 2, "16-bit types");
+  const int vpr = W6 >> 3;
+  const long long total = static_cast<long long>(N) * C * H6 * vpr;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long row = i / vpr;  // (plane, y) of the output
+    const int v = static_cast<int>(i - row * vpr);
+    const long long plane = row / H6;
+    const int y = static_cast<int>(row - plane * H6);
+    const T* src = in + (static_cast<size_t>(plane) * H + 2 * y) * W + 16 * v;
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(src));
+    const uint4 b = __ldg(reinterpret_cast<const uint4*>(src + 8));
+    // keep the low 16 bits of every 32-bit word (the even elements)
+    uint4 o;
+    o.x = __byte_perm(a.x, a.y, 0x5410);
+    o.y = __byte_perm(a.z, a.w, 0x5410);
+    o.z = __byte_perm(b.x, b.y, 0x5410);
+    o.w = __byte_perm(b.z, b.w, 0x5410);
+    *reinterpret_cast<uint4*>(out + static_cast<size_t>(row) * W6 + 8 * v) = o;
   }
 }
 
@@ -953,8 +1026,20 @@ cudaError_t upsample_add_t(const void* coarse, const void* lat, void* out, int N
   } else {
     const long long work = static_cast<long long>(N) * C * H * W;
     if (sc) return cudaErrorNotSupported;
-    cudaError_t e0 = launch_ex(upsample_add_nchw_kernel<T>, dim3(grid_for(work, 256)), dim3(256),
-                               0, s, opts, 1, c, l, o, N, C, Hc, Wc, H, W, sy, sx, ac);
+    cudaError_t e0;
+    if constexpr (sizeof(T) == 2) {
+      if (W % 8 == 0 && aligned16(out) && (lat == nullptr || aligned16(lat))) {
+        e0 = launch_ex(upsample_add_nchw_vec_kernel<T>, dim3(grid_for(work / 8, 256)), dim3(256),
+                       0, s, opts, 1, c, l, o, N, C, Hc, Wc, H, W, sy, sx, ac);
+        if (e0 != cudaSuccess) return e0;
+        e0 = cudaGetLastError();
+        if (e0 == cudaSuccess && amax)
+          e0 = absmax_t<T>(out, static_cast<long long>(N) * C * H * W, N, amax, s);
+        return e0;
+      }
+    }
+    e0 = launch_ex(upsample_add_nchw_kernel<T>, dim3(grid_for(work, 256)), dim3(256), 0, s, opts,
+                   1, c, l, o, N, C, Hc, Wc, H, W, sy, sx, ac);
     if (e0 != cudaSuccess) return e0;
   }
   cudaError_t e = cudaGetLastError();
@@ -980,6 +1065,12 @@ cudaError_t p6_t(const void* in, void* out, int N, int C, int H, int W, Layout l
       p6_nhwc_kernel<T, false><<<grid, 256, 0, s>>>(i, o, N, C, H, W, H6, W6);
   } else {
     const long long work = static_cast<long long>(N) * C * H6 * W6;
+    if constexpr (sizeof(T) == 2) {
+      if (W % 16 == 0 && aligned16(in) && aligned16(out)) {
+        p6_nchw_vec_kernel<T><<<grid_for(work / 8, 256), 256, 0, s>>>(i, o, N, C, H, W, H6, W6);
+        return cudaGetLastError();
+      }
+    }
     p6_nchw_kernel<T><<<grid_for(work, 256), 256, 0, s>>>(i, o, N, C, H, W, H6, W6);
   }
   return cudaGetLastError();

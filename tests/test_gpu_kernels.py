@@ -52,7 +52,9 @@ def test_upsample_nchw_fp32_matches_reference_golden(cuda_device, case):
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("layout", ["nhwc", "nchw"])
 @pytest.mark.parametrize("sizes", [((2, 256, 25, 38), (50, 76)), ((1, 256, 84, 50), (167, 100)),
-                                   ((1, 40, 7, 9), (13, 18))])
+                                   ((1, 40, 7, 9), (13, 18)),
+                                   ((2, 64, 20, 24), (40, 48)),      # NCHW rows of 8-element vectors
+                                   ((1, 32, 13, 21), (25, 40))])     # ... with a non-2x width
 def test_upsample_add(cuda_device, dtype, layout, sizes):
     import unified_fpn as U
     (n, c, hc, wc), (h, w) = sizes
@@ -127,13 +129,15 @@ def test_upsample_engine_abi(cuda_device, tmp_path):
 # ----------------------------------------------------------------------------- P6
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("layout", ["nhwc", "nchw"])
-def test_p6_exact(cuda_device, dtype, layout):
+@pytest.mark.parametrize("hw", [(25, 38), (20, 32), (7, 48)])  # (20, 32), (7, 48): NCHW 16-wide rows
+def test_p6_exact(cuda_device, dtype, layout, hw):
     import unified_fpn as U
-    p5 = torch.randn(2, 256, 25, 38).to(dtype).to(cuda_device)
+    h, w = hw
+    p5 = torch.randn(2, 256, h, w).to(dtype).to(cuda_device)
     if layout == "nhwc":
         p5 = _cl(p5)
     p6 = U.fpn_p6(p5)
-    assert p6.shape == (2, 256, 13, 19)
+    assert p6.shape == (2, 256, (h + 1) // 2, (w + 1) // 2)
     assert torch.equal(p6.cpu(), O.p6_maxpool(p5.cpu().float()).to(dtype))
 
 
