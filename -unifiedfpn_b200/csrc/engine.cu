@@ -177,6 +177,10 @@ struct UnifiedFPNCore::Impl {
   bool trace_next = false;
   unsigned long long last_trace[8] = {};
   cudaStream_t side = nullptr;
+  cudaStream_t p2_side = nullptr;  // the P2 3x3s of an image-pipelined P2 level
+  static constexpr int kMaxP2Parts = 8;
+  cudaEvent_t ev_p2[kMaxP2Parts] = {};
+  cudaEvent_t ev_p2_join = nullptr;
   cudaStream_t lat_side[2] = {};  // e4m3: the P4 and P3 laterals beside the P5 one
   cudaEvent_t ev_lat_done[2] = {};
   cudaStream_t capture = nullptr;
@@ -375,6 +379,12 @@ struct UnifiedFPNCore::Impl {
     d_status = nullptr;
     d_sched = nullptr;  // same allocation
     if (side) cudaStreamDestroy(side);
+    if (p2_side) cudaStreamDestroy(p2_side);
+    p2_side = nullptr;
+    for (auto& e : ev_p2)
+      if (e) cudaEventDestroy(e);
+    if (ev_p2_join) cudaEventDestroy(ev_p2_join);
+    ev_p2_join = nullptr;
     if (capture) cudaStreamDestroy(capture);
     if (setup) cudaStreamDestroy(setup);
     side = capture = setup = nullptr;
@@ -667,27 +677,61 @@ struct UnifiedFPNCore::Impl {
         if (prof_events) prof_record(4 + 2 * (2 - l), main);
       }
     }
-    TcPlan lat2;
-    // p2_pair: CTA pairs with resident weight halves and fp32 top-down taps (when the level
-    // qualifies: Cin <= 256, taps within a 64-pixel box); else one CTA per tile with the
-    // top-down add as a tensor-core k-block.
-    const cudaError_t pe =
-        p2_pair ? ufpn::plan_tc_lateral_pair(lat2, dtype, x[0], lat_wp[0], lat_b[0], merged[1],
-                                             merged[0], batch, cin[0], H[0], W[0], H[1], W[1],
-                                             lv[0].lat_tiling, d_status, 0)
-                : cudaErrorNotSupported;
-    if (pe != cudaSuccess) {
-      if (pe != cudaErrorNotSupported) check(pe, "plan lateral pair");
-      check(ufpn::plan_tc_lateral(lat2, dtype, x[0], lat_wp[0], lat_b[0], merged[1], merged[0],
-                                  batch, cin[0], H[0], W[0], H[1], W[1], lv[0].lat_tiling,
-                                  d_status, 0),
-            "plan lateral");
-      ufpn::tc_attach_wb_table(lat2, wb_table);
+    // The P2 lateral of images [n0, n0 + nb) (all its maps are NHWC with whole images
+    // contiguous, so an image group is a pointer offset).
+    auto launch_lat2 = [&](int n0, int nb, const ufpn::LaunchOpts& lo) {
+      const size_t px0 = static_cast<size_t>(n0) * H[0] * W[0];
+      const size_t px1 = static_cast<size_t>(n0) * H[1] * W[1];
+      const size_t esz = ufpn::dtype_size(dtype);
+      const void* xin = static_cast<const char*>(x[0]) + px0 * cin[0] * esz;
+      const void* m3 = static_cast<const char*>(merged[1]) + px1 * cout * esz;
+      void* m2 = static_cast<char*>(merged[0]) + px0 * cout * esz;
+      TcPlan lat2;
+      // p2_pair: CTA pairs with resident weight halves and fp32 top-down taps (when the level
+      // qualifies: Cin <= 256, taps within a 64-pixel box); else one CTA per tile with the
+      // top-down add as a tensor-core k-block.
+      const cudaError_t pe =
+          p2_pair ? ufpn::plan_tc_lateral_pair(lat2, dtype, xin, lat_wp[0], lat_b[0], m3, m2, nb,
+                                               cin[0], H[0], W[0], H[1], W[1], lv[0].lat_tiling,
+                                               d_status, 0)
+                  : cudaErrorNotSupported;
+      if (pe != cudaSuccess) {
+        if (pe != cudaErrorNotSupported) check(pe, "plan lateral pair");
+        check(ufpn::plan_tc_lateral(lat2, dtype, xin, lat_wp[0], lat_b[0], m3, m2, nb, cin[0],
+                                    H[0], W[0], H[1], W[1], lv[0].lat_tiling, d_status, 0),
+              "plan lateral");
+        ufpn::tc_attach_wb_table(lat2, wb_table);
+        if (cfg.lateral_wide_epilogue) ufpn::tc_use_wide_epilogue(lat2);
+      }
+      ok(ufpn::launch_tc(lat2, main, lo), "lateral launch");
+    };
+    const int parts = one_stream ? 1 : std::min({cfg.p2_parts, batch, Impl::kMaxP2Parts});
+    if (parts <= 1) {
+      launch_lat2(0, batch, chain);
+      if (prof_events) prof_record(7, main);
+      conv_level(0);
+      if (prof_events) prof_record(8, main);
+    } else {
+      // Image groups: group g's lateral on the main stream, its 3x3 on p2_side after an
+      // event, so the 3x3 of group g overlaps the lateral of group g + 1.
+      for (int g = 0; g < parts; ++g) {
+        const int n0 = batch * g / parts, n1 = batch * (g + 1) / parts;
+        launch_lat2(n0, n1 - n0, chain);
+        check(cudaEventRecord(ev_p2[g], main), "event");
+        check(cudaStreamWaitEvent(p2_side, ev_p2[g], 0), "event");
+        const size_t px0 = static_cast<size_t>(n0) * H[0] * W[0];
+        const size_t esz = ufpn::dtype_size(dtype);
+        TcPlan conv;
+        check(ufpn::plan_tc_conv3x3(conv, dtype, static_cast<char*>(merged[0]) + px0 * cout * esz,
+                                    out_wp[0], out_b[0], static_cast<char*>(o[0]) + px0 * cout * esz,
+                                    nullptr, n1 - n0, H[0], W[0], tiling_for(0), d_status, 0,
+                                    act_scales()),
+              "plan conv3x3");
+        ok(ufpn::launch_tc(conv, p2_side), "conv3x3 launch");
+      }
+      check(cudaEventRecord(ev_p2_join, p2_side), "event");
+      check(cudaStreamWaitEvent(main, ev_p2_join, 0), "event");
     }
-    ok(ufpn::launch_tc(lat2, main, chain), "lateral launch");
-    if (prof_events) prof_record(7, main);
-    conv_level(0);
-    if (prof_events) prof_record(8, main);
     if (!one_stream) join_conv_streams(main);
     if (nchw) {
       for (int l = 0; l < 4; ++l)
@@ -902,6 +946,9 @@ UnifiedFPNCore::UnifiedFPNCore(size_t workspace_size, int device) : impl_(new Im
   impl_->workspace_cap = workspace_size;
   DeviceGuard g(device);
   CUDA_CHECK(cudaStreamCreateWithFlags(&impl_->side, cudaStreamNonBlocking));
+  CUDA_CHECK(cudaStreamCreateWithFlags(&impl_->p2_side, cudaStreamNonBlocking));
+  for (auto& e : impl_->ev_p2) CUDA_CHECK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  CUDA_CHECK(cudaEventCreateWithFlags(&impl_->ev_p2_join, cudaEventDisableTiming));
   {
     int least = 0, greatest = 0;
     CUDA_CHECK(cudaDeviceGetStreamPriorityRange(&least, &greatest));
@@ -1356,6 +1403,10 @@ const std::vector<EngineOption>& engine_options() {
     o.push_back(bool_option<&FPNKernelConfig::single_stream>("single_stream"));
     o.push_back(bool_option<&FPNKernelConfig::fused_neck_kernel>("fused_neck_kernel"));
     o.push_back(bool_option<&FPNKernelConfig::fp8_two_pass_p2>("fp8_two_pass_p2"));
+    o.push_back(bool_option<&FPNKernelConfig::lateral_wide_epilogue>("lateral_wide_epilogue"));
+    o.push_back({"p2_parts", [](int v) { return v >= 0 && v <= 8; },
+                 [](UnifiedFPNCore::Impl& m, int v) { m.cfg.p2_parts = v; },
+                 [](const UnifiedFPNCore::Impl& m) { return m.cfg.p2_parts; }});
     for (int l = 1; l < 4; ++l) {
       static const char* names[4] = {"", "ksplit_p3", "ksplit_p4", "ksplit_p5"};
       o.push_back({names[l], [](int v) { return v == 1 || v == 2 || v == 4; },
@@ -1481,6 +1532,8 @@ std::string UnifiedFPNCore::autotune(const void* const* in, void* const* out, vo
     knobs.push_back({"ksplit_p4", {1, 2, 4}});
     knobs.push_back({"ksplit_p3", {1, 2}});
     knobs.push_back({"programmatic_launch", {1, 0}});
+    knobs.push_back({"lateral_wide_epilogue", {0, 1}});
+    if (m.batch >= 2) knobs.push_back({"p2_parts", {0, 2, std::min(m.batch, 4)}});
   } else {
     knobs.push_back({"fp8_two_pass_p2", {0, 1}});
   }

@@ -193,29 +193,37 @@ __device__ __forceinline__ void neck_tile_origin(const NeckJob& jb, int local, i
   y0 = ty * jb.tile_h;
 }
 
-constexpr int kNeckOffB = kNeckStages * kTcAStage;
-constexpr int kNeckOffStaging = kNeckOffB + kNeckStages * kTcBStage;
 constexpr int kNeckCoarseBlk = kTcCoarseMaxPix * 128;
-constexpr int kNeckOffCoarse = kNeckOffStaging + kTcEpiWarps * kTcStagingPerWarp;
-constexpr int kNeckOffBars = kNeckOffCoarse + 4 * kNeckCoarseBlk;
-constexpr int kNeckSmemBytes = kNeckOffBars + 512 + 1024;
-static_assert(kNeckSmemBytes <= 232448, "neck smem");
+// Shared-memory plan of fpn_neck_kernel: kStages operand stages, the epilogue staging and
+// (kCoarse) the 32 KB coarse box of the lateral top-down taps.  A launch with no staged
+// coarse box (the grouped raw laterals) trades that box for a fourth stage: per-tile
+// timestamps showed its 32- and 16-k-block lateral tiles waiting on operand latency with 3.
+template <int kStages, bool kCoarse>
+struct NeckCfg {
+  static constexpr int kOffB = kStages * kTcAStage;
+  static constexpr int kOffStaging = kOffB + kStages * kTcBStage;
+  static constexpr int kOffCoarse = kOffStaging + kTcEpiWarps * kTcStagingPerWarp;
+  static constexpr int kOffBars = kOffCoarse + (kCoarse ? 4 * kNeckCoarseBlk : 0);
+  static constexpr int kSmemBytes = kOffBars + 512 + 1024;
+  static_assert(kSmemBytes <= 232448, "neck smem");
+};
 
 constexpr int kDevTimeoutDependency = 0x105;
 
-template <typename T>
+template <typename T, int kStages = kNeckStages, bool kCoarse = true>
 __global__ void __launch_bounds__(kTcThreads, 1)
     fpn_neck_kernel(const __grid_constant__ NeckParams P) {
-  constexpr int S = kNeckStages;
+  using Cfg = NeckCfg<kStages, kCoarse>;
+  constexpr int S = kStages;
   constexpr int R = kNeckRing;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint8_t* smem_a = smem;
-  uint8_t* smem_b = smem + kNeckOffB;
-  uint8_t* smem_stage = smem + kNeckOffStaging;
-  uint8_t* smem_coarse = smem + kNeckOffCoarse;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kNeckOffBars);
+  uint8_t* smem_b = smem + Cfg::kOffB;
+  uint8_t* smem_stage = smem + Cfg::kOffStaging;
+  uint8_t* smem_coarse = smem + Cfg::kOffCoarse;  // (kCoarse only)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBars);
   uint64_t* full_bar = bars;
   uint64_t* empty_bar = bars + S;
   uint64_t* accf_bar = bars + 2 * S;
@@ -442,7 +450,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // Leader: wait_dep, then load the coarse box of lateral tile `t` of job `jb`.
     auto request_coarse = [&](const NeckJob& jb, int t) -> bool {
       if (!wait_dep(jb)) return false;
-      if (jb.cbox_w > 0) {
+      if (kCoarse && jb.cbox_w > 0) {
         int n, x0, y0;
         neck_tile_origin(jb, t - jb.tile_start, n, x0, y0);
         const int cy = static_cast<int>(tc_src(y0, jb.scale_y, jb.Hc));
@@ -470,7 +478,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const NeckJob& jb = P.jobs[neck_find_job(P, t)];
       const bool lateral = jb.mode == 0;
       const bool has_coarse = lateral && jb.coarse != nullptr;
-      const bool staged = has_coarse && jb.cbox_w > 0;
+      const bool staged = kCoarse && has_coarse && jb.cbox_w > 0;
       const bool split = lateral && jb.ksplit > 1;  // (split jobs never stage a coarse box)
       int part = 0;
       const int ptile = neck_unit_tile(jb, t - jb.tile_start, part);

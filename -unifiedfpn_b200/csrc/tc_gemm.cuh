@@ -93,11 +93,12 @@ constexpr int kMmaPerKb = 4;                                   // 32-byte K step
 // 2-k-block loop per tile, so its time per tile is the epilogue's latency chain (TMEM ->
 // registers -> scale -> bf16 -> staging -> TMA store) rather than the MMAs: it runs 16
 // epilogue warps, each owning 64 of the 256 output channels, and pays for their staging
-// with one operand stage.  (Measured per tile: 16-bit laterals, with 4 k-blocks, are
-// faster with 8 epilogue warps and 4 stages.)
-template <int kMode, typename T>
+// with one operand stage.  kWideEpi selects the same plan for a 16-bit lateral (an option:
+// per-tile timestamps of the P2 lateral, K = 256, showed its 8-warp epilogue at 3.3 us per
+// tile against a 2.9 us main loop).
+template <int kMode, typename T, bool kWideEpi = kMode == 0 && TcElem<T>::kFp8>
 struct TcCfgT {
-  static constexpr bool kWide = kMode == 0 && TcElem<T>::kFp8;
+  static constexpr bool kWide = kMode == 0 && kWideEpi;
   static constexpr int kEpiWarps = kWide ? 16 : kTcEpiWarps;
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
   static constexpr int kStages = kWide ? 3 : kTcStages;
@@ -649,13 +650,13 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
   __syncwarp();
 }
 
-template <int kMode, typename T>
-__global__ void __launch_bounds__(TcCfgT<kMode, T>::kThreads, 1)
+template <int kMode, typename T, bool kWideEpi = kMode == 0 && TcElem<T>::kFp8>
+__global__ void __launch_bounds__(TcCfgT<kMode, T, kWideEpi>::kThreads, 1)
     fpn_tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
                        const __grid_constant__ CUtensorMap map_b,
                        const __grid_constant__ CUtensorMap map_out,
                        const __grid_constant__ CUtensorMap map_coarse, const TcGemmArgs args) {
-  using Cfg = TcCfgT<kMode, T>;
+  using Cfg = TcCfgT<kMode, T, kWideEpi>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);

@@ -138,17 +138,19 @@ void fill_tiling(TcGemmArgs& a, int N, int H, int W, Conv3x3Tiling t) {
   a.tiles_y = (H + t.tile_h - 1) / t.tile_h;
 }
 
-template <int kMode, typename T>
+template <int kMode, typename T, bool kWideEpi = kMode == 0 && TcElem<T>::kFp8>
 cudaError_t launch_t(const TcPlan& p, cudaStream_t s, LaunchOpts opts) {
+  using Cfg = TcCfgT<kMode, T, kWideEpi>;
+  auto kern = fpn_tc_gemm_kernel<kMode, T, kWideEpi>;
   static std::atomic<bool> configured[64];
-  cudaError_t e = once_per_device(configured, [] {
-    return cudaFuncSetAttribute(fpn_tc_gemm_kernel<kMode, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfgT<kMode, T>::kSmemBytes);
+  cudaError_t e = once_per_device(configured, [&] {
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
   });
   if (e != cudaSuccess) return e;
   TcGemmArgs a;
   std::memcpy(&a, p.args, sizeof(a));
-  return launch_ex(fpn_tc_gemm_kernel<kMode, T>, dim3(p.grid), dim3(TcCfgT<kMode, T>::kThreads),
-                   TcCfgT<kMode, T>::kSmemBytes, s, opts, 1, p.map_a, p.map_b, p.map_out,
+  return launch_ex(kern, dim3(p.grid), dim3(Cfg::kThreads),
+                   Cfg::kSmemBytes, s, opts, 1, p.map_a, p.map_b, p.map_out,
                    p.map_coarse, a);
 }
 
@@ -493,6 +495,12 @@ cudaError_t tc_set_channel_slices(TcPlan& plan, const void* w, int K, int slices
   return cudaSuccess;
 }
 
+bool tc_use_wide_epilogue(TcPlan& plan) {
+  if (plan.mode != 0 || (plan.dtype != DType::BF16 && plan.dtype != DType::F16)) return false;
+  plan.mode = 6;
+  return true;
+}
+
 bool tc_attach_wb_table(TcPlan& plan, const void* table) {
   TcGemmArgs a;
   std::memcpy(&a, plan.args, sizeof(a));
@@ -683,16 +691,26 @@ cudaError_t plan_neck(NeckPlan& plan, DType dt, int N, const NeckLevel* lv, void
 }
 
 namespace {
-template <typename T>
-cudaError_t launch_neck_t(const NeckPlan& p, cudaStream_t s, LaunchOpts opts) {
+template <typename T, int kStages, bool kCoarse>
+cudaError_t launch_neck_cfg(const NeckPlan& p, cudaStream_t s, LaunchOpts opts) {
+  using Cfg = NeckCfg<kStages, kCoarse>;
+  auto kern = fpn_neck_kernel<T, kStages, kCoarse>;
   static std::atomic<bool> configured[64];
-  cudaError_t e = once_per_device(configured, [] {
-    return cudaFuncSetAttribute(fpn_neck_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kNeckSmemBytes);
+  cudaError_t e = once_per_device(configured, [&] {
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
   });
   if (e != cudaSuccess) return e;
   const NeckParams* P = reinterpret_cast<const NeckParams*>(p.params);
-  return launch_ex(fpn_neck_kernel<T>, dim3(p.grid), dim3(kTcThreads), kNeckSmemBytes, s, opts,
-                   1, *P);
+  return launch_ex(kern, dim3(p.grid), dim3(kTcThreads), Cfg::kSmemBytes, s, opts, 1, *P);
+}
+template <typename T>
+cudaError_t launch_neck_t(const NeckPlan& p, cudaStream_t s, LaunchOpts opts) {
+  // Four operand stages when no job stages a coarse box (its buffer is not needed), else three.
+  const NeckParams* P = reinterpret_cast<const NeckParams*>(p.params);
+  bool coarse_box = false;
+  for (int j = 0; j < P->num_jobs; ++j) coarse_box |= P->jobs[j].mode == 0 && P->jobs[j].cbox_w > 0;
+  return coarse_box ? launch_neck_cfg<T, kNeckStages, true>(p, s, opts)
+                    : launch_neck_cfg<T, kNeckStages + 1, false>(p, s, opts);
 }
 }  // namespace
 
@@ -722,6 +740,10 @@ cudaError_t launch_tc(const TcPlan& plan, cudaStream_t s, LaunchOpts opts) {
   if (plan.mode == 0) {
     return plan.dtype == DType::BF16 ? launch_t<0, __nv_bfloat16>(plan, s, opts)
                                      : launch_t<0, __half>(plan, s, opts);
+  }
+  if (plan.mode == 6) {  // 16-bit lateral with the 16-warp epilogue
+    return plan.dtype == DType::BF16 ? launch_t<0, __nv_bfloat16, true>(plan, s, opts)
+                                     : launch_t<0, __half, true>(plan, s, opts);
   }
   if (plan.mode == 2) {
     return plan.dtype == DType::BF16 ? launch_halo_t<__nv_bfloat16>(plan, s, opts)

@@ -230,6 +230,45 @@ def e2e_ceiling(dev, h2d_bytes, d2h_bytes, steps, images_per_step):
     return ms, images_per_step * steps
 
 
+def run_bandwidth_kernels(args, dev):
+    """--kernels bandwidth: the standalone HBM-bound ops on maps larger than the 126 MB L2
+    (bf16): the top-down upsample-add (NHWC: the merge kernel of the neck; NCHW) and P6 (NHWC,
+    NCHW); per op the CUDA-event time of one call (after warm-up), algorithmic bytes (compulsory
+    reads + writes) and GB/s against the measured HBM copy bandwidth.  One JSON line."""
+    import unified_fpn as U
+    peaks = measured_peaks()
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(11)
+    cl = torch.channels_last
+    res = {}
+
+    def run(name, fn, nbytes):
+        ms = time_steps(fn, max(1, args.steps), warmup=max(3, args.warmup))
+        res[name] = {"us": round(ms * 1e3, 1), "mb": round(nbytes / 1e6, 1),
+                     "gb_s": round(nbytes / (ms * 1e-3) / 1e9, 0),
+                     "frac_of_hbm": round(nbytes / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4)}
+
+    c = torch.randn(4, 256, 200, 304, device=dev, generator=gen).to(torch.bfloat16)
+    l = torch.randn(4, 256, 400, 608, device=dev, generator=gen).to(torch.bfloat16)
+    nb = 2 * l.numel() * 2 + c.numel() * 2  # read lateral + coarse, write the sum
+    cn, ln = c.contiguous(memory_format=cl), l.contiguous(memory_format=cl)
+    run("upsample_add_nhwc_4x256x400x608", lambda: U.fpn_upsample_add(cn, ln), nb)
+    run("upsample_add_nchw_4x256x400x608", lambda: U.fpn_upsample_add(c, l), nb)
+    del c, l, cn, ln
+    p5 = torch.randn(16, 256, 200, 304, device=dev, generator=gen).to(torch.bfloat16)
+    p5c = p5.contiguous(memory_format=cl)
+    nb6 = p5.numel() * 2 // 2  # read the even pixels of the even rows (1/4), write them (1/4)
+    run("p6_nhwc_16x256x200x304", lambda: U.fpn_p6(p5c), nb6)
+    run("p6_nchw_16x256x200x304", lambda: U.fpn_p6(p5), nb6)
+    line = {"metric": "HBM-bound neck ops, GB/s on maps larger than L2 (bf16)", "value": None,
+            "unit": "GB/s", "n_gpus": 1, "higher_is_better": True, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1))", "peak_hbm_gbs": peaks["hbm_gbs"],
+            "peak_src": peaks["src"], "kernels": res}
+    line["value"] = min(v["gb_s"] for v in res.values())
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def measured_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -480,6 +519,9 @@ def main():
                          "per-level kernels one after the other on one stream")
     ap.add_argument("--train", action="store_true",
                     help="time the training step (FPNNeck forward + backward) instead")
+    ap.add_argument("--kernels", choices=["bandwidth"], default=None,
+                    help="bandwidth: time the standalone HBM-bound ops (upsample-add, P6) on "
+                         "maps larger than L2 instead (one JSON line, GB/s per op)")
     ap.add_argument("--graph", action="store_true",
                     help="with --train: replay the step as CUDA graphs (FPNNeck.make_graphed)")
     args = ap.parse_args()
@@ -512,6 +554,8 @@ def main():
 
     if args.train:
         return run_train(args, rank, world, local, dev)
+    if args.kernels == "bandwidth":
+        return run_bandwidth_kernels(args, dev)
     fp8 = args.dtype == "e4m3"
     dtype = {"bf16": torch.bfloat16, "fp16": torch.float16, "e4m3": torch.float8_e4m3fn}[args.dtype]
     esz = 1 if fp8 else 2

@@ -182,6 +182,14 @@ struct FPNKernelConfig {
   // the forward ends with status kDevTimeoutDependency (outputs undefined) and the engine
   // must recover after device_status(reset).  No fault, trap or hang is involved.
   int test_stall_dependency_us = 0;
+  // 16-bit P2 lateral (one CTA per tile): 16 epilogue warps and 3 operand stages instead of 8
+  // warps and 4 stages (bitwise the same results).
+  bool lateral_wide_epilogue = false;
+  // 16-bit split schedule: the P2 level (its lateral and 3x3) pipelined over this many groups
+  // of images (0 or 1: one launch each for the whole batch).  Group g's 3x3 runs on a second
+  // stream while group g + 1's lateral runs, so the P2 3x3 starts after one group's lateral
+  // instead of the whole batch's.
+  int p2_parts = 0;
 };
 
 struct FPNWeights {

@@ -138,7 +138,8 @@ struct TcPlan {
   alignas(64) CUtensorMap map_coarse;
   unsigned char args[256];  // TcGemmArgs, opaque outside tc_kernels.cu
   int mode = 0;  // 0 lateral, 1 conv3x3, 2 conv3x3 halo, 3 halo on CTA pairs, 4 the same + e4m3
-                 // quantisation of a bf16 input in shared memory, 5 lateral on CTA pairs
+                 // quantisation of a bf16 input in shared memory, 5 lateral on CTA pairs,
+                 // 6 16-bit lateral with a 16-warp epilogue
   DType dtype = DType::BF16;
   int grid = 0;
   int num_tiles = 0;
@@ -204,6 +205,10 @@ size_t tc_wb_table_bytes(int H, int W, int Hc, int Wc, Conv3x3Tiling t);
 cudaError_t tc_build_wb_table(DType dt, int H, int W, int Hc, int Wc, Conv3x3Tiling t,
                               void* table, cudaStream_t s);
 bool tc_attach_wb_table(TcPlan& plan, const void* table);
+// 16-bit lateral plans: 16 epilogue warps (64 output channels each) and 3 operand stages
+// instead of 8 warps and 4 stages; same results bitwise.  Returns false (plan unchanged)
+// for other plans.
+bool tc_use_wide_epilogue(TcPlan& plan);
 // Tiled NHWC tensor map with 128-byte swizzle: dims (C, W, H, N), pixel stride pix_stride
 // elements (>= C), box (one 128-byte row of channels, bw, bh, 1).
 cudaError_t encode_nhwc_map(CUtensorMap* map, DType dt, const void* base, int N, int H, int W,
