@@ -8,6 +8,12 @@
 // which read both CTAs' shared memory and write each CTA's 128 accumulator lanes in its
 // own TMEM.
 //
+// Tail items (args.pair_tail > 0): when the last round of pair units would leave pairs idle,
+// each of the last pair_tail units runs as two items over the output channels (M = 256,
+// N = 128; each CTA stages 64 rows of every weight k-block through map_bh, a 64-row box),
+// so the last round takes about half as long.  Each output element accumulates over the
+// same K order either way: the results are bitwise those of whole units.
+//
 // Synchronisation (all waits bounded, as everywhere in this library):
 //   full[s], hfull[h]  leader's barriers; the leader's producer arms them with BOTH CTAs'
 //                      byte counts, both producers' TMA loads complete on them
@@ -67,6 +73,7 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
     fpn_conv3x3_halo_pair_kernel(const __grid_constant__ CUtensorMap map_a,
                                  const __grid_constant__ CUtensorMap map_b,
                                  const __grid_constant__ CUtensorMap map_out,
+                                 const __grid_constant__ CUtensorMap map_bh,
                                  const TcGemmArgs args) {
   static_assert(!kCvt || TcElem<T>::kFp8, "the converter quantises to e4m3");
   using Cfg = PairCfgT<kCvt>;
@@ -98,6 +105,7 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
   const bool leader = rank == 0;
   const int cin_blocks = args.cin_blocks;
   const int units = (args.num_tiles + 1) / 2;
+  const int items = units + args.pair_tail;  // work items (pair_item_unit)
   const int u0 = static_cast<int>(blockIdx.x >> 1);
   const int ustep = static_cast<int>(gridDim.x >> 1);
 
@@ -122,6 +130,7 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
     prefetch_tmap(&map_a);
     prefetch_tmap(&map_b);
     prefetch_tmap(&map_out);
+    if (args.pair_tail > 0) prefetch_tmap(&map_bh);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, kTcTmemCols);
@@ -141,9 +150,15 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
       bool ok = true;
       const uint32_t full0 = mapa_shared(smem_u32(full_bar), 0);
       const uint32_t hfull0 = mapa_shared(smem_u32(hfull_bar), 0);
-      const int brow = static_cast<int>(rank) * (kTcBlockN / 2);
       uint32_t rphase = 0;
-      for (int u = u0; ok && u < units; u += ustep) {
+      for (int it = u0; ok && it < items; it += ustep) {
+        int half;
+        const int u = pair_item_unit(args, units, it, half);
+        // weight rows this CTA stages per k-block: 128 of 256, or 64 of a half's 128
+        const int brow = half < 0 ? static_cast<int>(rank) * (kTcBlockN / 2)
+                                  : half * (kTcBlockN / 2) + static_cast<int>(rank) * (kTcBlockN / 4);
+        const CUtensorMap* mb = half < 0 ? &map_b : &map_bh;
+        const uint32_t bbytes = half < 0 ? 2 * kPairBStage : kPairBStage;  // both CTAs
         int n, x0, y0;
         tc_tile_origin(args, 2 * u + static_cast<int>(rank), n, x0, y0);
         for (int cb = 0; ok && cb < cin_blocks; ++cb) {
@@ -179,8 +194,8 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
               ok = false;
               break;
             }
-            if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * kPairBStage);
-            tma_load_2d_pair(smem_b + stage * kPairBStage, &map_b, full0 + stage * 8u,
+            if (leader) mbar_arrive_expect_tx(&full_bar[stage], bbytes);
+            tma_load_2d_pair(smem_b + stage * kPairBStage, mb, full0 + stage * 8u,
                              (tap * cin_blocks + cb) * kKbElems<T>, brow, kPolicyEvictLast);
             if (++stage == S) {
               stage = 0;
@@ -197,12 +212,17 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (leader)
     if (leader && lane == 0) {
-      constexpr uint32_t idesc =
+      constexpr uint32_t idesc_full =
           make_idesc(2 * kTcBlockM, kTcBlockN, TcElem<T>::kFmt, TcElem<T>::kFmt);
+      constexpr uint32_t idesc_half =
+          make_idesc(2 * kTcBlockM, kTcBlockN / 2, TcElem<T>::kFmt, TcElem<T>::kFmt);
       int stage = 0, hb = 0, acc = 0;
       uint32_t phase = 0, hphase = 0, acc_phase = 0;
       bool ok = true;
-      for (int u = u0; ok && u < units; u += ustep) {
+      for (int it = u0; ok && it < items; it += ustep) {
+        int half;
+        pair_item_unit(args, units, it, half);
+        const uint32_t idesc = half < 0 ? idesc_full : idesc_half;
         if (!mbar_wait(&acce_bar[acc], acc_phase ^ 1u, abort_flag, args.status, kDevTimeoutMma))
           break;
         tc_fence_after();
@@ -265,8 +285,9 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
     int hb = 0;
     uint32_t hphase = 0, rphase = 0;
     bool ok = true;
-    for (int u = u0; ok && u < units; u += ustep) {
-      const int tile = 2 * u + static_cast<int>(rank);
+    for (int it = u0; ok && it < items; it += ustep) {
+      int half;
+      const int tile = 2 * pair_item_unit(args, units, it, half) + static_cast<int>(rank);
       int n, x0, y0;
       tc_tile_origin(args, tile, n, x0, y0);
       // virtual tile (past the end): its halo is all padding, any finite scale will do

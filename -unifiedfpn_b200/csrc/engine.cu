@@ -198,6 +198,8 @@ struct UnifiedFPNCore::Impl {
   int wb_tile_w = 0;            // lateral tile width the Wb table was built for
   bool p2_pair = false;         // 16-bit P2 lateral on CTA pairs (resident weight halves)
   int merge_units = 0;          // units per block of the merge kernels (0: automatic)
+  int p2_lateral_ctas = 0;      // CTAs of the 16-bit P2 lateral (0: one per SM)
+  bool p2_lateral_dynamic = false;  // 16-bit P2 lateral as a one-job neck launch (tile claims)
   bool profiling = false;
   FPNPerformanceMetrics metrics{};
   struct GraphEntry {
@@ -434,7 +436,9 @@ struct UnifiedFPNCore::Impl {
       t.tile_h = 128 / cfg.tile_size;
       return t;
     }
-    return tiling[l];
+    Conv3x3Tiling t = tiling[l];
+    t.tail_halves = cfg.conv3x3_tail_halves;
+    return t;
   }
 
   void check(cudaError_t e, const char* what) {
@@ -634,7 +638,10 @@ struct UnifiedFPNCore::Impl {
       lv[l].split_sem = split_sem ? split_sem + split_sem_off[l] : nullptr;
     }
     auto ks = [&](int l) { return split_part[l] ? split_alloc[l] : 1; };
-    const ufpn::NeckJobSpec grouped[3] = {{0, 3, 0, ks(3)}, {0, 2, td, ks(2)}, {0, 1, td, ks(1)}};
+    // channel halves: raw laterals (no top-down add in the launch) without split-K only
+    auto ns = [&](int l) { return ks(l) == 1 && (l == 3 || !td) ? cfg.lateral_nsplit[l] : 1; };
+    const ufpn::NeckJobSpec grouped[3] = {
+        {0, 3, 0, ks(3), ns(3)}, {0, 2, td, ks(2), ns(2)}, {0, 1, td, ks(1), ns(1)}};
     ufpn::NeckPlan gplan;
     check(ufpn::plan_neck_jobs(gplan, dtype, batch, lv, nullptr, grouped, 3, d_sched, d_status, 0,
                                trace_next ? d_trace : nullptr),
@@ -680,6 +687,18 @@ struct UnifiedFPNCore::Impl {
     // The P2 lateral of images [n0, n0 + nb) (all its maps are NHWC with whole images
     // contiguous, so an image group is a pointer offset).
     auto launch_lat2 = [&](int n0, int nb, const ufpn::LaunchOpts& lo) {
+      if (p2_lateral_dynamic && n0 == 0 && nb == batch) {
+        // One lateral job (P2, top-down add of M3 from a staged coarse box, fp32 taps) on the
+        // neck kernel: CTAs claim tiles from a counter, so CTAs that start late (their SMs
+        // held by a 3x3 of another level) take fewer tiles.  Own schedule counters.
+        const ufpn::NeckJobSpec job[1] = {{0, 0, 1}};
+        ufpn::NeckPlan p2plan;
+        check(ufpn::plan_neck_jobs(p2plan, dtype, batch, lv, nullptr, job, 1, d_sched + 16,
+                                   d_status, p2_lateral_ctas),
+              "plan P2 lateral");
+        ok(ufpn::launch_neck(p2plan, main, lo), "P2 lateral launch");
+        return;
+      }
       const size_t px0 = static_cast<size_t>(n0) * H[0] * W[0];
       const size_t px1 = static_cast<size_t>(n0) * H[1] * W[1];
       const size_t esz = ufpn::dtype_size(dtype);
@@ -693,12 +712,13 @@ struct UnifiedFPNCore::Impl {
       const cudaError_t pe =
           p2_pair ? ufpn::plan_tc_lateral_pair(lat2, dtype, xin, lat_wp[0], lat_b[0], m3, m2, nb,
                                                cin[0], H[0], W[0], H[1], W[1], lv[0].lat_tiling,
-                                               d_status, 0)
+                                               d_status, p2_lateral_ctas)
                   : cudaErrorNotSupported;
       if (pe != cudaSuccess) {
         if (pe != cudaErrorNotSupported) check(pe, "plan lateral pair");
         check(ufpn::plan_tc_lateral(lat2, dtype, xin, lat_wp[0], lat_b[0], m3, m2, nb, cin[0],
-                                    H[0], W[0], H[1], W[1], lv[0].lat_tiling, d_status, 0),
+                                    H[0], W[0], H[1], W[1], lv[0].lat_tiling, d_status,
+                                    p2_lateral_ctas),
               "plan lateral");
         ufpn::tc_attach_wb_table(lat2, wb_table);
         if (cfg.lateral_wide_epilogue) ufpn::tc_use_wide_epilogue(lat2);
@@ -1029,6 +1049,8 @@ void UnifiedFPNCore::configure_levels(const std::vector<FPNDimensions>& dims, in
   }
   m.p2_pair = false;
   m.merge_units = 0;
+  m.p2_lateral_ctas = 0;
+  m.p2_lateral_dynamic = false;
   m.apply_tuning_db2();  // a whole-neck tuning of this geometry, if any
   const size_t esz = ufpn::dtype_size(dt);
   const size_t msz = dt == DType::E4M3 ? 2 : esz;  // merged maps: bf16 for e4m3 inputs
@@ -1404,6 +1426,7 @@ const std::vector<EngineOption>& engine_options() {
     o.push_back(bool_option<&FPNKernelConfig::fused_neck_kernel>("fused_neck_kernel"));
     o.push_back(bool_option<&FPNKernelConfig::fp8_two_pass_p2>("fp8_two_pass_p2"));
     o.push_back(bool_option<&FPNKernelConfig::lateral_wide_epilogue>("lateral_wide_epilogue"));
+    o.push_back(bool_option<&FPNKernelConfig::conv3x3_tail_halves>("conv3x3_tail_halves"));
     o.push_back({"p2_parts", [](int v) { return v >= 0 && v <= 8; },
                  [](UnifiedFPNCore::Impl& m, int v) { m.cfg.p2_parts = v; },
                  [](const UnifiedFPNCore::Impl& m) { return m.cfg.p2_parts; }});
@@ -1412,6 +1435,10 @@ const std::vector<EngineOption>& engine_options() {
       o.push_back({names[l], [](int v) { return v == 1 || v == 2 || v == 4; },
                    [l](UnifiedFPNCore::Impl& m, int v) { m.cfg.lateral_ksplit[l] = v; },
                    [l](const UnifiedFPNCore::Impl& m) { return m.cfg.lateral_ksplit[l]; }});
+      static const char* halves[4] = {"", "nsplit_p3", "nsplit_p4", "nsplit_p5"};
+      o.push_back({halves[l], [](int v) { return v == 1 || v == 2; },
+                   [l](UnifiedFPNCore::Impl& m, int v) { m.cfg.lateral_nsplit[l] = v; },
+                   [l](const UnifiedFPNCore::Impl& m) { return m.cfg.lateral_nsplit[l]; }});
     }
     for (int l = 0; l < 4; ++l) {
       static const char* lat[4] = {"lateral_tile_p2", "lateral_tile_p3", "lateral_tile_p4",
@@ -1430,6 +1457,12 @@ const std::vector<EngineOption>& engine_options() {
     o.push_back({"p2_lateral_pair", in01,
                  [](UnifiedFPNCore::Impl& m, int v) { m.p2_pair = v != 0; },
                  [](const UnifiedFPNCore::Impl& m) { return m.p2_pair ? 1 : 0; }});
+    o.push_back({"p2_lateral_dynamic", in01,
+                 [](UnifiedFPNCore::Impl& m, int v) { m.p2_lateral_dynamic = v != 0; },
+                 [](const UnifiedFPNCore::Impl& m) { return m.p2_lateral_dynamic ? 1 : 0; }});
+    o.push_back({"p2_lateral_ctas", [](int v) { return v >= 0 && v <= 4096; },
+                 [](UnifiedFPNCore::Impl& m, int v) { m.p2_lateral_ctas = v; },
+                 [](const UnifiedFPNCore::Impl& m) { return m.p2_lateral_ctas; }});
     o.push_back({"merge_units", [](int v) { return v >= 0 && v <= 256; },
                  [](UnifiedFPNCore::Impl& m, int v) { m.merge_units = v; },
                  [](const UnifiedFPNCore::Impl& m) { return m.merge_units; }});
@@ -1531,6 +1564,9 @@ std::string UnifiedFPNCore::autotune(const void* const* in, void* const* out, vo
     knobs.push_back({"ksplit_p5", {1, 2, 4}});
     knobs.push_back({"ksplit_p4", {1, 2, 4}});
     knobs.push_back({"ksplit_p3", {1, 2}});
+    knobs.push_back({"nsplit_p5", {1, 2}});
+    knobs.push_back({"nsplit_p4", {1, 2}});
+    knobs.push_back({"nsplit_p3", {1, 2}});
     knobs.push_back({"programmatic_launch", {1, 0}});
     knobs.push_back({"lateral_wide_epilogue", {0, 1}});
     if (m.batch >= 2) knobs.push_back({"p2_parts", {0, 2, std::min(m.batch, 4)}});

@@ -28,6 +28,13 @@
 // epilogue.  Each add is commutative, so the bits do not depend on which unit arrives last:
 // results are deterministic.  The last unit resets the semaphore for the next launch.
 //
+// Channel-half lateral tiles (job.nsplit == 2): a tile is cut into two units over its output
+// channels (N = 128 each: a 128-row weight box, an N = 128 MMA, half the epilogue), numbered
+// consecutively so that two CTAs stream the tile's pixels side by side (the second read hits
+// L2).  Each unit streams half the weight bytes of a whole tile and issues half its MMA
+// work, so a deep-K tile (the P5 lateral) holds an SM about half as long, with no partial
+// sums to reduce.  Every unit stores and publishes its own half.
+//
 // Cross-CTA visibility: an epilogue waits for its own TMA stores to complete
 // (cp.async.bulk.wait_group 0), fences the async proxy, synchronises the
 // epilogue warps and publishes with a release add; consumers acquire the
@@ -77,6 +84,7 @@ struct NeckJob {
   int act;                 // conv3x3: output activation after the bias (0 = none)
   float act_alpha;
   int ksplit;              // lateral: units per tile over K (1 = whole tiles)
+  int nsplit;              // lateral: units per tile over the output channels (1 or 2)
   int kb_per;              // k-blocks per unit (the last unit of a tile may have fewer)
   float* part;             // ksplit > 1: fp32 partials, [unit][256 columns][128 rows]
   int* sem;                // ksplit > 1: per-tile arrival counters (zero between launches)
@@ -159,19 +167,27 @@ __device__ __forceinline__ int neck_find_job(const NeckParams& p, int t) {
   return j;
 }
 
-// Unit `local` of a job -> its pixel tile and (split-K jobs) its part of the K loop.
+// Unit `local` of a job -> its pixel tile and its part: of the K loop (split-K jobs) or of
+// the output channels (channel-half jobs); a job splits one way at most.
 __device__ __forceinline__ int neck_unit_tile(const NeckJob& jb, int local, int& part) {
-  if (jb.ksplit <= 1) {
+  const int per = jb.ksplit * jb.nsplit;
+  if (per <= 1) {
     part = 0;
     return local;
   }
-  const int pt = local / jb.ksplit;
-  part = local - pt * jb.ksplit;
+  const int pt = local / per;
+  part = local - pt * per;
   return pt;
 }
+// (a channel-half unit's part names its channels: it runs the whole K loop)
 __device__ __forceinline__ void neck_unit_kb(const NeckJob& jb, int part, int& kb0, int& kb1) {
+  if (jb.ksplit <= 1) {
+    kb0 = 0;
+    kb1 = jb.num_kb;
+    return;
+  }
   kb0 = part * jb.kb_per;
-  kb1 = jb.ksplit <= 1 ? jb.num_kb : min(jb.num_kb, kb0 + jb.kb_per);
+  kb1 = min(jb.num_kb, kb0 + jb.kb_per);
 }
 __device__ __forceinline__ int atom_acq_rel_gpu_add(int* p, int v) {
   int old;
@@ -322,7 +338,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full_bar[stage], kTcAStage + kTcBStage);
+          mbar_arrive_expect_tx(&full_bar[stage], kTcAStage + kTcBStage / jb.nsplit);
           int dy = 0, dx = 0, cb = kb;
           if (jb.mode == 1) {
             const int tap = kb / jb.cin_blocks;
@@ -332,8 +348,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
           tma_load_4d(smem_a + stage * kTcAStage, &jb.map_a, &full_bar[stage], cb * kTcBlockK,
                       x0 + dx, y0 + dy, n, jb.mode == 0 ? kPolicyEvictFirst : kPolicyEvictLast);
-          tma_load_2d(smem_b + stage * kTcBStage, &jb.map_b, &full_bar[stage], kb * kTcBlockK, 0,
-                      kPolicyEvictLast);
+          // (channel halves: a 128-row box of the unit's output channels)
+          tma_load_2d(smem_b + stage * kTcBStage, &jb.map_b, &full_bar[stage], kb * kTcBlockK,
+                      jb.nsplit > 1 ? part * (kTcBlockN / 2) : 0, kPolicyEvictLast);
           if (kb == kb1 - 1) t_next = atomicAdd(&sched[0], 1);
           ++issued;
           if (++stage == S) {
@@ -361,7 +378,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc(kTcBlockM, kTcBlockN, Pack<T>::kFmt, Pack<T>::kFmt);
+      constexpr uint32_t idesc_full =
+          make_idesc(kTcBlockM, kTcBlockN, Pack<T>::kFmt, Pack<T>::kFmt);
+      constexpr uint32_t idesc_half =
+          make_idesc(kTcBlockM, kTcBlockN / 2, Pack<T>::kFmt, Pack<T>::kFmt);
       int stage = 0;
       uint32_t phase = 0;
       int rslot = 0;
@@ -383,6 +403,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         neck_unit_tile(jm, t - jm.tile_start, mpart);
         neck_unit_kb(jm, mpart, kb0, kb1);
         const int num_kb = kb1 - kb0;
+        const uint32_t idesc = jm.nsplit > 1 ? idesc_half : idesc_full;
         if (P.trace && jm.mode == 1 && jm.level == 0 && t == jm.tile_start)
           P.trace[6] = globaltimer_ns();
         if (!mbar_wait(&acce_bar[acc], acc_phase ^ 1u, abort_flag, P.status, kDevTimeoutMma))
@@ -619,17 +640,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int ox = x0 + (wrow0 % tw);
       const int oy = y0 + wrow0 / tw;
 
+      // This warp's accumulator columns: 128 of a whole tile (two 64-column steps), 64 of a
+      // channel-half unit (whose N = 128 accumulator starts at the buffer's column 0 and
+      // holds output channels part * 128 ..).
+      const int nsteps = 2 / jb.nsplit;
+      const int ocol = jb.nsplit > 1 ? part * (kTcBlockN / 2) : 0;
 #pragma unroll 1
-      for (int step = 0; step < 2; ++step) {
-        const int col0 = chalf * 128 + step * 64;
+      for (int step = 0; step < nsteps; ++step) {
+        const int tcol = chalf * 64 * nsteps + step * 64;
+        const int col0 = ocol + tcol;  // output channel of the step's first column
         uint32_t r[64];
         __syncwarp();
-        const uint32_t taddr = tmem_base + static_cast<uint32_t>(acc * kTcBlockN + col0) +
+        const uint32_t taddr = tmem_base + static_cast<uint32_t>(acc * kTcBlockN + tcol) +
                                (static_cast<uint32_t>(quarter * 32) << 16);
         tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
         tmem_ld32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
         tmem_wait_ld();
-        if (step == 1) {
+        if (step == nsteps - 1) {
           tc_fence_before();
           mbar_arrive(&acce_bar[acc]);
         }

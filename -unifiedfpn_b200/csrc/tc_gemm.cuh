@@ -170,7 +170,24 @@ struct TcGemmArgs {
   // output activation after the bias (FPNActivation numbering; 0 = none) and its alpha
   int act;
   float act_alpha;
+  // 3x3 on CTA pairs: the last pair_tail pair units each run as two work items over the
+  // output channels (N = 128: channels 0..127, then 128..255), so that a last round with
+  // fewer units than pairs takes half as long (0 = every unit whole)
+  int pair_tail;
 };
+
+// Work items of a CTA-pair 3x3: units [0, units - pair_tail) whole (half = -1), then two
+// channel-half items per tail unit.  Returns the item's pair unit.
+__device__ __forceinline__ int pair_item_unit(const TcGemmArgs& a, int units, int item,
+                                              int& half) {
+  const int first = units - a.pair_tail;
+  if (item < first) {
+    half = -1;
+    return item;
+  }
+  half = (item - first) & 1;
+  return first + ((item - first) >> 1);
+}
 
 template <typename T>
 struct Pack;
@@ -420,9 +437,12 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
   uint32_t acc_phase = 0;
   const int rank = kPair ? static_cast<int>(cluster_ctarank()) : 0;
   const int units = kPair ? (args.num_tiles + 1) / 2 : args.num_tiles;
+  const int items = kPair ? units + args.pair_tail : units;
   const int ustep = kPair ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
-  for (int u = kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
-       u < units; u += ustep) {
+  for (int it = kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+       it < items; it += ustep) {
+    int half = -1;  // channel-half item of a CTA-pair 3x3 (its accumulator has N = 128)
+    const int u = kPair ? pair_item_unit(args, units, it, half) : it;
     const int tile = kPair ? 2 * u + rank : u;
     const bool real = tile < args.num_tiles;
     const bool ok =
@@ -480,10 +500,15 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
     const int ox = x0 + (wrow0 % tw);
     const int oy = y0 + wrow0 / tw;
 
+    // A channel-half item: kChans / 2 accumulator columns per warp, output channels from
+    // half * 128 (kSteps is even wherever items are halved: 8 epilogue warps).
+    const int nsteps = half < 0 ? kSteps : kSteps / 2;
+    const int tcol0 = half < 0 ? chalf * kChans : chalf * (kChans / 2);
+    const int ocol0 = half < 0 ? tcol0 : half * (kTcBlockN / 2) + tcol0;
 #pragma unroll 1
-    for (int step = 0; step < kSteps; ++step) {
-      const int col0 = chalf * kChans + step * 64;
-      const uint32_t taddr = tmem_base + static_cast<uint32_t>(acc * kTcBlockN + col0) +
+    for (int step = 0; step < nsteps; ++step) {
+      const int col0 = ocol0 + step * 64;  // output channel of the step's first column
+      const uint32_t taddr = tmem_base + static_cast<uint32_t>(acc * kTcBlockN + tcol0 + step * 64) +
                              (static_cast<uint32_t>(quarter * 32) << 16);
       // With 8 epilogue warps (registers to spare), both 32-column halves of the step are
       // loaded from TMEM with one wait: the loads overlap each other and the staging-buffer
@@ -515,18 +540,18 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
       const uint32_t stage_addr = smem_u32(my_stage + sbuf * kTcStagingPerWarp);
       if constexpr (kBoth) {
         tmem_wait_ld();
-        if (step == kSteps - 1) release_acc();
+        if (step == nsteps - 1) release_acc();
       }
       // Two 32-column halves per 64-channel step.
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const int c0 = col0 + half * 32;
-        const uint32_t* r = kBoth ? rr + half * 32 : rr;
+      for (int hh = 0; hh < 2; ++hh) {
+        const int c0 = col0 + hh * 32;
+        const uint32_t* r = kBoth ? rr + hh * 32 : rr;
         if constexpr (!kBoth) {
           __syncwarp();
-          tmem_ld32(taddr + half * 32, *reinterpret_cast<uint32_t(*)[32]>(&rr[0]));
+          tmem_ld32(taddr + hh * 32, *reinterpret_cast<uint32_t(*)[32]>(&rr[0]));
           tmem_wait_ld();
-          if (step == kSteps - 1 && half == 1) release_acc();
+          if (step == nsteps - 1 && hh == 1) release_acc();
         }
         float v[32];
         const float4* b4 = reinterpret_cast<const float4*>(args.bias + scol + c0);
@@ -579,7 +604,7 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
         __syncwarp();
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
-          const int j = half * 4 + jj;  // 16-byte chunk of the 128-byte staging row
+          const int j = hh * 4 + jj;  // 16-byte chunk of the 128-byte staging row
           uint4 o;
           o.x = Pack<O>::pack(v[8 * jj + 0], v[8 * jj + 1]);
           o.y = Pack<O>::pack(v[8 * jj + 2], v[8 * jj + 3]);

@@ -176,9 +176,10 @@ cudaError_t launch_halo_pair_t(const TcPlan& p, cudaStream_t s, LaunchOpts opts)
   if (e != cudaSuccess) return e;
   TcGemmArgs a;
   std::memcpy(&a, p.args, sizeof(a));
+  // (map_coarse of a CTA-pair 3x3 plan: the 64-row weight box of its channel-half items)
   return launch_ex(fpn_conv3x3_halo_pair_kernel<T, kCvt>, dim3(p.grid),
                    dim3(PairCfgT<kCvt>::kThreads), PairCfgT<kCvt>::kSmemBytes, s, opts, 2,
-                   p.map_a, p.map_b, p.map_out, a);
+                   p.map_a, p.map_b, p.map_out, p.map_coarse, a);
 }
 
 template <typename T>
@@ -375,7 +376,6 @@ cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w
   if ((e = encode_nhwc(&plan.map_out, odt, out, N, H, W, kTcBlockN, sw, 32 / sw)) != cudaSuccess)
     return e;
   plan.map_coarse = plan.map_out;
-  std::memcpy(plan.args, &a, sizeof(a));
   plan.mode = cvt ? 4 : (tiling.pair ? 3 : (halo ? 2 : 1));
   plan.dtype = dt;
   plan.num_tiles = a.num_tiles;
@@ -385,9 +385,18 @@ cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w
     const int units = (a.num_tiles + 1) / 2;
     const int clusters = units < cap / 2 ? units : cap / 2;
     plan.grid = 2 * (clusters > 0 ? clusters : 1);
+    // A last round of rem < clusters units: if its units split over the output channels fit
+    // the pairs (2 rem <= clusters), run them as halves (N = 128), half as long a round.
+    const int rem = clusters > 0 ? units % clusters : 0;
+    if (tiling.tail_halves && rem > 0 && 2 * rem <= clusters) {
+      a.pair_tail = rem;
+      if ((e = encode_weights(&plan.map_coarse, dt, w, 9 * C, kTcBlockN / 4)) != cudaSuccess)
+        return e;
+    }
   } else {
     plan.grid = a.num_tiles < cap ? a.num_tiles : cap;
   }
+  std::memcpy(plan.args, &a, sizeof(a));
   return cudaSuccess;
 }
 
@@ -543,12 +552,18 @@ cudaError_t plan_neck_jobs(NeckPlan& plan, DType dt, int N, const NeckLevel* lv,
       if (L.Cin <= 0 || L.Cin % 8 != 0 || !aligned16(L.lat_b)) return cudaErrorInvalidValue;
       if (lat_in_launch[s.level]) return cudaErrorInvalidValue;
       if (s.ksplit != 1 && s.ksplit != 2 && s.ksplit != 4) return cudaErrorInvalidValue;
+      if (s.nsplit != 1 && (s.nsplit != 2 || s.ksplit != 1 || s.coarse))
+        return cudaErrorInvalidValue;
       const int cin_blocks = (L.Cin + kTcBlockK - 1) / kTcBlockK;
       if (s.ksplit > 1 && (cin_blocks < s.ksplit || !L.split_part || !L.split_sem ||
                            !aligned16(L.split_part)))
         return cudaErrorInvalidValue;
       lat_in_launch[s.level] = true;
-      lat_tiles[s.level] = ((L.W + t.tile_w - 1) / t.tile_w) * ((L.H + t.tile_h - 1) / t.tile_h) * N;
+      // (completions counted per publishing unit: a channel half publishes its own half)
+      lat_tiles[s.level] =
+          ((L.W + t.tile_w - 1) / t.tile_w) * ((L.H + t.tile_h - 1) / t.tile_h) * N * s.nsplit;
+    } else if (s.ksplit != 1 || s.nsplit != 1) {
+      return cudaErrorInvalidValue;
     } else if (!aligned16(L.out) || !aligned16(L.conv_b)) {
       return cudaErrorMisalignedAddress;
     }
@@ -584,6 +599,11 @@ cudaError_t plan_neck_jobs(NeckPlan& plan, DType dt, int N, const NeckLevel* lv,
       J.num_kb = J.cin_blocks;
       J.bias = L.lat_b;
       J.ksplit = specs[j].ksplit;
+      J.nsplit = specs[j].nsplit;
+      if (J.nsplit > 1) {
+        start += J.num_tiles * (J.nsplit - 1);  // units = tiles x channel halves
+        J.num_tiles *= J.nsplit;
+      }
       if (J.ksplit > 1) {
         // ceil(num_kb / ksplit) k-blocks per unit; every unit gets at least one
         J.kb_per = (J.num_kb + J.ksplit - 1) / J.ksplit;
@@ -598,7 +618,9 @@ cudaError_t plan_neck_jobs(NeckPlan& plan, DType dt, int N, const NeckLevel* lv,
       if ((e = encode_nhwc(&J.map_a, dt, L.x, N, L.H, L.W, L.Cin, t.tile_w, t.tile_h)) !=
           cudaSuccess)
         return e;
-      if ((e = encode_weights(&J.map_b, dt, L.lat_w, L.Cin)) != cudaSuccess) return e;
+      if ((e = encode_weights(&J.map_b, dt, L.lat_w, L.Cin, kTcBlockN / J.nsplit)) !=
+          cudaSuccess)
+        return e;
       if ((e = encode_nhwc(&J.map_out, dt, L.merged, N, L.H, L.W, kTcBlockN, sw, 32 / sw)) !=
           cudaSuccess)
         return e;
@@ -628,6 +650,7 @@ cudaError_t plan_neck_jobs(NeckPlan& plan, DType dt, int N, const NeckLevel* lv,
       J.num_kb = 9 * J.cin_blocks;
       J.kb_per = J.num_kb;
       J.ksplit = 1;
+      J.nsplit = 1;
       J.bias = L.conv_b;
       if (L.act < 0 || L.act > 3) return cudaErrorInvalidValue;
       J.act = L.act;

@@ -177,6 +177,12 @@ struct FPNKernelConfig {
   // lateral runs in its own kernel and ignores its entry): 1, 2 or 4.  A long K loop (the P5
   // lateral's 2048 channels) otherwise holds one SM per tile for its whole weight stream.
   int lateral_ksplit[4] = {1, 1, 1, 1};
+  // Units per lateral tile over the output channels in the grouped lateral launch, per level
+  // (P2..P5; P2 ignored): 1, or 2 (two N = 128 halves, each streaming half the weights; a
+  // level with lateral_ksplit > 1 keeps whole-channel units).
+  int lateral_nsplit[4] = {1, 1, 1, 1};
+  // 3x3 on CTA pairs: run a short last round of pair units as channel halves (N = 128 each).
+  bool conv3x3_tail_halves = true;
   // Self-test of the device's bounded waits (0 = off): on the fused schedule, the P2 3x3
   // waits for a lateral tile that never comes, with a limit of this many microseconds, so
   // the forward ends with status kDevTimeoutDependency (outputs undefined) and the engine

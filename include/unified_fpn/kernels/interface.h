@@ -113,6 +113,9 @@ struct Conv3x3Tiling {
   // Halo tiles on CTA pairs (tcgen05 cta_group::2, M = 256 per MMA): each CTA streams
   // half of every weight k-block.
   bool pair = false;
+  // CTA pairs: a last round with at most half as many units as pairs runs each of its
+  // units as two halves over the output channels (N = 128), in half the time (same bits).
+  bool tail_halves = true;
 };
 // The 3x3 default: halo reuse with 8 x 16 tiles.
 inline Conv3x3Tiling halo_tiling() {
@@ -275,12 +278,14 @@ cudaError_t plan_neck(NeckPlan& plan, DType dt, int N, const NeckLevel* levels, 
 // level+1's merged map), mode 1 = 3x3 of `level`.  A job waits on a level only if that
 // level's lateral runs in the same launch; otherwise its input must be complete before.
 // ksplit (laterals): 1, 2 or 4 units per tile over K, each at least one k-block long; > 1
-// needs the level's split_part / split_sem workspace.
+// needs the level's split_part / split_sem workspace.  nsplit (laterals without a top-down
+// add, ksplit 1): 1, or 2 units per tile over the output channels (128 each).
 struct NeckJobSpec {
   int mode;
   int level;
   int coarse;
   int ksplit = 1;
+  int nsplit = 1;
 };
 cudaError_t plan_neck_jobs(NeckPlan& plan, DType dt, int N, const NeckLevel* levels, void* p6,
                            const NeckJobSpec* specs, int num_specs, int* sched, int* status,

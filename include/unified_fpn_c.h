@@ -148,6 +148,15 @@ int ufpn_core_set_schedule_options(ufpn_core* core, int programmatic_launch, int
  *   "ksplit_p3", "ksplit_p4", "ksplit_p5"
  *                       1/2/4 units per lateral tile over K in that launch (a last-arriving
  *                            unit sums the fp32 partials in a fixed order: deterministic)
+ *   "p2_lateral_ctas"  0..4096  CTAs of the 16-bit P2 lateral (0 = one per SM): fewer leave
+ *                            SMs to the P3 / P4 3x3s running beside it
+ *   "conv3x3_tail_halves"  0/1  (default 1) a 3x3 on CTA pairs runs a last round of at most
+ *                            half as many units as pairs as channel halves (N = 128), in half
+ *                            the time; the same bits
+ *   "nsplit_p3", "nsplit_p4", "nsplit_p5"
+ *                         1/2  units per lateral tile over the output channels in that
+ *                            launch (two N = 128 halves: half the weight stream per unit, the
+ *                            same bits; ignored for a level with ksplit > 1 or a top-down add)
  *   "test_stall_dependency_us"  0..1000000  self-test of the device's bounded waits (0 =
  *                            off): on the fused schedule the P2 3x3 waits for a lateral tile
  *                            that never comes, for this many microseconds, then the forward

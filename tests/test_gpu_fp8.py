@@ -110,7 +110,7 @@ def test_lateral_fp8_matches_oracle(cuda_device, geom):
 
 
 @pytest.mark.parametrize("per_image", [False, True])
-@pytest.mark.parametrize("shape", [(2, 40, 56), (1, 25, 38), (3, 13, 21)])
+@pytest.mark.parametrize("shape", [(2, 40, 56), (1, 25, 38), (3, 13, 21), (1, 200, 304)])
 def test_conv3x3_fp8_matches_oracle(cuda_device, shape, per_image):
     import unified_fpn as U
     N, H, W = shape
@@ -141,10 +141,12 @@ def test_conv3x3_fp8_matches_oracle(cuda_device, shape, per_image):
     assert torch.equal(p6.cpu(), out[:, :, ::2, ::2].cpu())
 
 
-@pytest.mark.parametrize("shape", [(2, 40, 56), (1, 25, 38), (3, 13, 21), (16, 160, 160)])
+@pytest.mark.parametrize("shape", [(2, 40, 56), (1, 25, 38), (3, 13, 21), (16, 160, 160),
+                                   (1, 200, 304)])
 def test_conv3x3_fp8_in_kernel_quantisation(cuda_device, shape):
     """The CTA-pair e4m3 3x3 that quantises its bf16 input per image in shared memory gives
-    bitwise what quantising first (the standalone quantiser) and convolving gives."""
+    bitwise what quantising first (the standalone quantiser) and convolving gives (1 x 200 x
+    304: 247 pair units, the last 25 as channel halves on 148 SMs)."""
     import unified_fpn as U
     N, H, W = shape
     g = torch.Generator(device="cuda").manual_seed(15)

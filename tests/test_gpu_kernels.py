@@ -264,12 +264,14 @@ def test_conv3x3_tc_with_p6(cuda_device, dtype, shape):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("shape", [(1, 16, 8), (1, 13, 21), (2, 25, 38), (3, 17, 5), (1, 1, 1),
-                                   (2, 200, 304)])
+                                   (2, 200, 304), (1, 200, 304)])
 def test_conv3x3_cta_pair_equals_single(cuda_device, dtype, shape):
     """Halo tiles on CTA pairs (tcgen05 cta_group::2, M = 256: two tiles per MMA stream, each
     CTA streaming half of the weights) give bitwise the results of single-CTA halo tiles:
     every output's K summation runs in the same order.  Odd tile counts exercise the
-    virtual (never stored) second tile of the last pair; (2, 200, 304) is the R50 P2 map."""
+    virtual (never stored) second tile of the last pair; (2, 200, 304) is the R50 P2 map.
+    On 148 SMs (74 pairs) the two 200x304 maps end with a short round (475 units: 31 left,
+    247: 25) that runs as channel halves (N = 128 items)."""
     import unified_fpn as U
     n, h, w_ = shape
     g = torch.Generator().manual_seed(h * 31 + w_)

@@ -389,7 +389,11 @@ RAGGED = [(52, 70), (26, 35), (13, 18), (7, 9)]
 @pytest.mark.parametrize("opts", [
     {}, {"fused_neck_kernel": 1}, {"grouped_topdown": 1}, {"ksplit_p5": 2, "ksplit_p4": 2},
     {"grouped_topdown": 1, "ksplit_p5": 4, "ksplit_p4": 2, "ksplit_p3": 2}, {"merge_two_levels": 1},
-], ids=["split", "fused", "grouped_topdown", "ksplit", "topdown_ksplit", "merge_two_levels"])
+    {"nsplit_p5": 2, "nsplit_p4": 2, "nsplit_p3": 2}, {"grouped_topdown": 1, "nsplit_p5": 2},
+    {"nsplit_p5": 2, "ksplit_p4": 2, "nsplit_p3": 2}, {"p2_lateral_dynamic": 1},
+    {"p2_lateral_dynamic": 1, "p2_lateral_ctas": 37},
+], ids=["split", "fused", "grouped_topdown", "ksplit", "topdown_ksplit", "merge_two_levels",
+        "nsplit", "topdown_nsplit", "nsplit_ksplit", "p2_dynamic", "p2_dynamic_37ctas"])
 def test_neck_ragged_tile_seams(cuda_device, opts):
     """Every schedule option on ragged maps against the oracle (max-norm and per-element),
     bitwise deterministic, and each image alone equals its slice of the batch."""
@@ -415,7 +419,8 @@ def test_neck_ragged_tile_seams(cuda_device, opts):
 
 
 @pytest.mark.parametrize("opts", [{"grouped_topdown": 1}, {"ksplit_p5": 4, "ksplit_p4": 2},
-                                  {"grouped_topdown": 1, "ksplit_p5": 2, "ksplit_p4": 2, "ksplit_p3": 2}])
+                                  {"grouped_topdown": 1, "ksplit_p5": 2, "ksplit_p4": 2, "ksplit_p3": 2},
+                                  {"p2_lateral_dynamic": 1}, {"p2_lateral_ctas": 74}])
 def test_grouped_launch_options_full_size(cuda_device, opts):
     """The grouped-lateral options at the R50 800x1216 batch-2 workload: the first image
     against the oracle, repeated launches bitwise equal (the split-K sum is order-free and the
@@ -440,6 +445,55 @@ def test_grouped_launch_options_full_size(cuda_device, opts):
     _check([o[:1] for o in outs], ref, torch.bfloat16)
 
 
+def test_channel_half_laterals_equal_whole_tiles_bitwise(cuda_device):
+    """Channel-half units (N = 128 MMAs over 128-row weight boxes) accumulate every output
+    element over the same K order as whole tiles: the neck is bitwise the same with and
+    without them, at the R50 800x1216 batch-2 workload, and matches the oracle."""
+    import unified_fpn as U
+    sizes = O.level_sizes(800, 1216)
+    host = O.make_features(2, O.R50_CHANNELS, sizes, seed=93)
+    wts = O.make_weights(O.R50_CHANNELS, seed=94, bias_scale=0.1)
+    xin = [_cl(f.to(torch.bfloat16).cuda()) for f in host]
+    res = []
+    for ns in (1, 2):
+        fpn = U.UnifiedFPN()
+        for lv in (3, 4, 5):
+            fpn.set_option(f"nsplit_p{lv}", ns)
+        fpn.initialize_weights(wts.lat_w, wts.lat_b, wts.out_w, wts.out_b)
+        res.append([o.clone() for o in _run(fpn, xin)])
+        assert fpn.device_status() == 0
+    assert all(torch.equal(a, b) for a, b in zip(*res))
+    rw = O.NeckWeights([O.round_to(w, torch.bfloat16) for w in wts.lat_w], wts.lat_b,
+                       [O.round_to(w, torch.bfloat16) for w in wts.out_w], wts.out_b)
+    ref = O.fpn_neck([O.round_to(f[:1], torch.bfloat16) for f in host], rw)
+    _check([o[:1] for o in res[1]], ref, torch.bfloat16)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_conv3x3_tail_halves_bitwise_at_full_size(cuda_device, dtype):
+    """The P2 3x3 on CTA pairs at the R50 800x1216 batch-2 workload ends with 31 of 475 pair
+    units on 74 pairs; run as channel halves (the default) the neck is bitwise what whole
+    units give (conv3x3_tail_halves=0), and matches the oracle."""
+    import unified_fpn as U
+    sizes = O.level_sizes(800, 1216)
+    host = O.make_features(2, O.R50_CHANNELS, sizes, seed=95)
+    wts = O.make_weights(O.R50_CHANNELS, seed=96, bias_scale=0.1)
+    xin = [_cl(f.to(dtype).cuda()) for f in host]
+    res = []
+    for on in (1, 0):
+        fpn = U.UnifiedFPN()
+        fpn.set_option("conv3x3_tail_halves", on)
+        assert fpn.get_option("conv3x3_tail_halves") == on
+        fpn.initialize_weights(wts.lat_w, wts.lat_b, wts.out_w, wts.out_b)
+        res.append([o.clone() for o in _run(fpn, xin)])
+        assert fpn.device_status() == 0
+    assert all(torch.equal(a, b) for a, b in zip(*res))
+    rw = O.NeckWeights([O.round_to(w, dtype) for w in wts.lat_w], wts.lat_b,
+                       [O.round_to(w, dtype) for w in wts.out_w], wts.out_b)
+    ref = O.fpn_neck([O.round_to(f[:1], dtype) for f in host], rw)
+    _check([o[:1] for o in res[0]], ref, dtype)
+
+
 def test_schedule_option_api_errors(cuda_device):
     import unified_fpn as U
     fpn = U.UnifiedFPN()
@@ -448,6 +502,8 @@ def test_schedule_option_api_errors(cuda_device):
         fpn.set_option("no_such_option", 1)
     with pytest.raises(RuntimeError):
         fpn.set_option("ksplit_p5", 3)
+    with pytest.raises(RuntimeError):
+        fpn.set_option("nsplit_p4", 4)
 
 
 def test_bounded_wait_runs_out_and_the_engine_recovers(cuda_device):
