@@ -211,6 +211,21 @@ int sm_count() {
   return n;
 }
 
+long long l2_bytes() {
+  static std::atomic<long long> sizes[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const bool cached = dev >= 0 && dev < 64;
+  long long n = cached ? sizes[dev].load(std::memory_order_relaxed) : 0;
+  if (n == 0) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrL2CacheSize, dev);
+    n = v > 0 ? v : 126LL << 20;
+    if (cached) sizes[dev].store(n, std::memory_order_relaxed);
+  }
+  return n;
+}
+
 Conv3x3Tiling default_tiling(int H, int W) {
   Conv3x3Tiling best;
   long long best_area = -1;

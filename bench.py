@@ -123,6 +123,57 @@ def time_steps(fn, steps, warmup=3, stream=None):
     return e0.elapsed_time(e1) / steps
 
 
+def cupti_timeline(fwd, n=14, skip=3):
+    """Per-kernel device timeline of the concurrent schedule: torch.profiler (CUPTI) over n
+    forwards, each followed by a synchronize so that forwards separate by an idle gap; the
+    first `skip` are dropped.  Per kernel (in start order within a forward): median start,
+    end and duration in us from the forward's first kernel start, and the median forward
+    span.  None if the profiler is unavailable (for instance CUPTI held by another tool)."""
+    import statistics
+    import tempfile
+    try:
+        from torch.profiler import ProfilerActivity, profile
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            for i in range(n):
+                fwd(i)
+                torch.cuda.synchronize()
+        with tempfile.TemporaryDirectory() as td:
+            path = os.path.join(td, "trace.json")
+            prof.export_chrome_trace(path)
+            with open(path) as f:
+                ev = [e for e in json.load(f)["traceEvents"] if e.get("cat") == "kernel"]
+    except Exception:
+        return None
+    ev.sort(key=lambda e: e["ts"])
+    fwds, end = [], None
+    for e in ev:  # a gap of > 15 us with no kernel running separates forwards
+        if end is None or e["ts"] > end + 15.0:
+            fwds.append([])
+        fwds[-1].append(e)
+        end = max(end or 0.0, e["ts"] + e["dur"])
+    fwds = fwds[skip:]
+    if not fwds:
+        return None
+    k = statistics.mode(len(f) for f in fwds)
+    fwds = [f for f in fwds if len(f) == k]
+    rows = []
+    for j in range(k):
+        name = fwds[0][j]["name"]
+        short = name.replace("(anonymous namespace)::", "").split("(")[0].replace(
+            "void ", "").replace("ufpn::", "")
+        st = [f[j]["ts"] - f[0]["ts"] for f in fwds]
+        du = [f[j]["dur"] for f in fwds]
+        rows.append({"kernel": short[:80], "start_us": round(statistics.median(st), 1),
+                     "end_us": round(statistics.median(s + d for s, d in zip(st, du)), 1),
+                     "us": round(statistics.median(du), 1)})
+    span = statistics.median(max(e["ts"] + e["dur"] for e in f) - f[0]["ts"] for f in fwds)
+    return {"forward_us": round(span, 1), "forwards": len(fwds), "kernels": rows,
+            "what": "CUPTI kernel records (torch.profiler) of the concurrent schedule, each forward "
+                    "followed by a synchronize; median over forwards; a kernel's duration includes "
+                    "the time it waits for SMs held by kernels of other streams and, under a "
+                    "programmatic launch, for the kernel before it"}
+
+
 def extra_workloads(dev, peaks):
     """The other configurations' per-GPU shards, timed in the same run (not the headline):
     each the whole neck through UnifiedFPN on device-resident inputs rotating over 2 sets,
@@ -720,6 +771,9 @@ def main():
         roofline["neck_frac_of_roofline"] = round(t_roof * 1e3 / ms_per_step, 4)
         roofline["neck_roofline_ms"] = round(t_roof * 1e3, 4)
 
+    kernel_timeline = None
+    if rank == 0 and world == 1 and not args.no_roofline:
+        kernel_timeline = cupti_timeline(step)
     timeline = None
     if args.schedule == "fused" and not args.no_roofline:
         timeline = {k: (round(v, 1) if v is not None else None)
@@ -754,6 +808,7 @@ def main():
             "kernel_time_share_what": "device time per stage of one forward with the stages serialised "
                                       "on one stream (replayed as a CUDA graph, events between stages; "
                                       "the concurrent schedule overlaps them)",
+            "kernel_timeline_us": kernel_timeline,
             "cpu_baseline": cpu,
             "device_status": status, "per_rank_ms_per_step": ranks_ms, "extra": extra,
         }

@@ -344,5 +344,7 @@ cudaError_t launch_flip_conv3x3_weights(DType dt, const void* w_packed, void* w_
 
 // Number of SMs on the current device (cached).
 int sm_count();
+// L2 size of the current device in bytes (cached per device).
+long long l2_bytes();
 
 }  // namespace ufpn

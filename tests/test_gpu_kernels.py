@@ -54,8 +54,12 @@ def test_upsample_nchw_fp32_matches_reference_golden(cuda_device, case):
 @pytest.mark.parametrize("sizes", [((2, 256, 25, 38), (50, 76)), ((1, 256, 84, 50), (167, 100)),
                                    ((1, 40, 7, 9), (13, 18)),
                                    ((2, 64, 20, 24), (40, 48)),      # NCHW rows of 8-element vectors
-                                   ((1, 32, 13, 21), (25, 40))])     # ... with a non-2x width
-def test_upsample_add(cuda_device, dtype, layout, sizes):
+                                   ((1, 32, 13, 21), (25, 40)),      # ... with a non-2x width
+                                   ((4, 256, 100, 77), (200, 153)),  # 256 ch, W % 8 = 1
+                                   ((2, 64, 100, 152), (200, 304)),  # NCHW 8-element vectors
+                                   ((1, 16, 64, 64), (24, 32)),      # ... downsampling (8 : 3)
+                                   ((2, 256, 200, 152), (400, 304))])  # 124 MB lateral > L2 / 2:
+def test_upsample_add(cuda_device, dtype, layout, sizes):          # interleaved NHWC batches
     import unified_fpn as U
     (n, c, hc, wc), (h, w) = sizes
     g = torch.Generator().manual_seed(5)
