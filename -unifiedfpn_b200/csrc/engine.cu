@@ -642,11 +642,31 @@ struct UnifiedFPNCore::Impl {
     auto ns = [&](int l) { return ks(l) == 1 && (l == 3 || !td) ? cfg.lateral_nsplit[l] : 1; };
     const ufpn::NeckJobSpec grouped[3] = {
         {0, 3, 0, ks(3), ns(3)}, {0, 2, td, ks(2), ns(2)}, {0, 1, td, ks(1), ns(1)}};
-    ufpn::NeckPlan gplan;
-    check(ufpn::plan_neck_jobs(gplan, dtype, batch, lv, nullptr, grouped, 3, d_sched, d_status, 0,
-                               trace_next ? d_trace : nullptr),
-          "plan grouped laterals");
-    ok(ufpn::launch_neck(gplan, main, nchw ? chain : chain_first), "grouped laterals launch");
+    // grouped_laterals_pair: the same raw laterals on CTA pairs (whole tiles only: no top-down
+    // add, split-K or channel halves in the launch; a geometry too large for its static plan
+    // falls back to the single-CTA launch).
+    bool pair_done = false;
+    if (cfg.grouped_laterals_pair && !td && ks(1) * ks(2) * ks(3) == 1 &&
+        ns(1) * ns(2) * ns(3) == 1) {
+      ufpn::LateralGroupPlan lplan;
+      const int which[3] = {3, 2, 1};
+      const cudaError_t pe =
+          ufpn::plan_lateral_group_pair(lplan, dtype, batch, lv, which, 3, d_status, 0);
+      if (pe == cudaSuccess) {
+        ok(ufpn::launch_lateral_group_pair(lplan, main, nchw ? chain : chain_first),
+           "grouped laterals (pairs) launch");
+        pair_done = true;
+      } else if (pe != cudaErrorNotSupported) {
+        check(pe, "plan grouped laterals (pairs)");
+      }
+    }
+    if (!pair_done) {
+      ufpn::NeckPlan gplan;
+      check(ufpn::plan_neck_jobs(gplan, dtype, batch, lv, nullptr, grouped, 3, d_sched, d_status,
+                                 0, trace_next ? d_trace : nullptr),
+            "plan grouped laterals");
+      ok(ufpn::launch_neck(gplan, main, nchw ? chain : chain_first), "grouped laterals launch");
+    }
     if (prof_events) prof_record(1, main);
     conv_level(3);
     if (prof_events) prof_record(2, main);
@@ -1427,6 +1447,7 @@ const std::vector<EngineOption>& engine_options() {
     o.push_back(bool_option<&FPNKernelConfig::fp8_two_pass_p2>("fp8_two_pass_p2"));
     o.push_back(bool_option<&FPNKernelConfig::lateral_wide_epilogue>("lateral_wide_epilogue"));
     o.push_back(bool_option<&FPNKernelConfig::conv3x3_tail_halves>("conv3x3_tail_halves"));
+    o.push_back(bool_option<&FPNKernelConfig::grouped_laterals_pair>("grouped_laterals_pair"));
     o.push_back({"p2_parts", [](int v) { return v >= 0 && v <= 8; },
                  [](UnifiedFPNCore::Impl& m, int v) { m.cfg.p2_parts = v; },
                  [](const UnifiedFPNCore::Impl& m) { return m.cfg.p2_parts; }});
@@ -1560,6 +1581,7 @@ std::string UnifiedFPNCore::autotune(const void* const* in, void* const* out, vo
   }
   if (!fp8) {
     if (m.cin[0] <= 256) knobs.push_back({"p2_lateral_pair", {0, 1}});
+    knobs.push_back({"grouped_laterals_pair", {0, 1}});
     knobs.push_back({"grouped_topdown", {0, 1}});
     knobs.push_back({"ksplit_p5", {1, 2, 4}});
     knobs.push_back({"ksplit_p4", {1, 2, 4}});

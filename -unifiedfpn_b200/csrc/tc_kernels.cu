@@ -2,12 +2,16 @@
 // planning and launch.  The device code lives in tc_gemm.cuh.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "conv_pair.cuh"
 #include "kernels.h"
+#include "lateral_group_pair.cuh"
 #include "lateral_pair.cuh"
 #include "neck_kernel.cuh"
 #include "tc_gemm.cuh"
@@ -751,6 +755,113 @@ cudaError_t launch_neck_t(const NeckPlan& p, cudaStream_t s, LaunchOpts opts) {
                     : launch_neck_cfg<T, kNeckStages + 1, false>(p, s, opts);
 }
 }  // namespace
+
+static_assert(sizeof(LgParams) <= sizeof(LateralGroupPlan::params),
+              "LateralGroupPlan::params too small");
+
+cudaError_t plan_lateral_group_pair(LateralGroupPlan& plan, DType dt, int N,
+                                    const NeckLevel* lv, const int* which, int count,
+                                    int* status, int max_ctas) {
+  if (dt != DType::BF16 && dt != DType::F16) return cudaErrorNotSupported;
+  if (N <= 0 || count < 1 || count > kLgMaxJobs || !which) return cudaErrorInvalidValue;
+  LgParams* P = reinterpret_cast<LgParams*>(plan.params);
+  std::memset(plan.params, 0, sizeof(plan.params));
+  // (job, units, k-blocks per unit)
+  struct JobUnits {
+    int job, units, kb;
+  };
+  std::vector<JobUnits> ju;
+  long long total_units = 0;
+  for (int j = 0; j < count; ++j) {
+    const int l = which[j];
+    if (l < 0 || l > 3) return cudaErrorInvalidValue;
+    const NeckLevel& L = lv[l];
+    const Conv3x3Tiling t = L.lat_tiling;
+    if (!valid_tiling(t) || L.H <= 0 || L.W <= 0 || L.Cin <= 0 || L.Cin % 8 != 0)
+      return cudaErrorInvalidValue;
+    if (!aligned16(L.merged) || !aligned16(L.lat_b)) return cudaErrorMisalignedAddress;
+    LgJob& J = P->jobs[j];
+    J.N_img = N;
+    J.H = L.H;
+    J.W = L.W;
+    J.tile_w = t.tile_w;
+    J.tile_h = t.tile_h;
+    J.tiles_x = (L.W + t.tile_w - 1) / t.tile_w;
+    J.tiles_y = (L.H + t.tile_h - 1) / t.tile_h;
+    const long long tiles = static_cast<long long>(J.tiles_x) * J.tiles_y * N;
+    if (tiles >= (1LL << 28)) return cudaErrorNotSupported;
+    J.num_tiles = static_cast<int>(tiles);
+    J.num_kb = (L.Cin + kTcBlockK - 1) / kTcBlockK;
+    J.bias = L.lat_b;
+    cudaError_t e;
+    if ((e = encode_nhwc(&J.map_a, dt, L.x, N, L.H, L.W, L.Cin, t.tile_w, t.tile_h)) !=
+        cudaSuccess)
+      return e;
+    if ((e = encode_weights(&J.map_b, dt, L.lat_w, L.Cin, kTcBlockN / 2)) != cudaSuccess)
+      return e;
+    const int sw = t.tile_w < 32 ? t.tile_w : 32;
+    if ((e = encode_nhwc(&J.map_out, dt, L.merged, N, L.H, L.W, kTcBlockN, sw, 32 / sw)) !=
+        cudaSuccess)
+      return e;
+    const int units = (J.num_tiles + 1) / 2;
+    if (units >= (1 << 14)) return cudaErrorNotSupported;
+    ju.push_back({j, units, J.num_kb});
+    total_units += units;
+  }
+  if (total_units > kLgMaxItems) return cudaErrorNotSupported;
+  const int cap = (max_ctas > 0 ? max_ctas : sm_count()) / 2;
+  const int pairs = static_cast<int>(std::min<long long>({total_units, cap, kLgMaxPairs}));
+  if (pairs <= 0) return cudaErrorInvalidValue;
+  // Longest first to the least-loaded pair (ties: the lowest pair), k-blocks as the load.
+  std::sort(ju.begin(), ju.end(), [](const JobUnits& a, const JobUnits& b) {
+    return a.kb != b.kb ? a.kb > b.kb : a.job < b.job;
+  });
+  std::vector<long long> load(pairs, 0);
+  std::vector<std::vector<unsigned short>> lists(pairs);
+  for (const JobUnits& x : ju)
+    for (int u = 0; u < x.units; ++u) {
+      int best = 0;
+      for (int p = 1; p < pairs; ++p)
+        if (load[p] < load[best]) best = p;
+      load[best] += x.kb;
+      lists[best].push_back(static_cast<unsigned short>((x.job << 14) | u));
+    }
+  int k = 0;
+  for (int p = 0; p < pairs; ++p) {
+    P->off[p] = static_cast<unsigned short>(k);
+    for (unsigned short it : lists[p]) P->items[k++] = it;
+  }
+  P->off[pairs] = static_cast<unsigned short>(k);
+  P->num_jobs = count;
+  P->num_pairs = pairs;
+  P->status = status;
+  plan.dtype = dt;
+  plan.grid = 2 * pairs;
+  return cudaSuccess;
+}
+
+namespace {
+template <typename T>
+cudaError_t launch_lateral_group_pair_t(const LateralGroupPlan& p, cudaStream_t s,
+                                        LaunchOpts opts) {
+  auto kern = fpn_lateral_group_pair_kernel<T>;
+  static std::atomic<bool> configured[64];
+  cudaError_t e = once_per_device(configured, [&] {
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                LgCfg::kSmemBytes);
+  });
+  if (e != cudaSuccess) return e;
+  const LgParams* P = reinterpret_cast<const LgParams*>(p.params);
+  return launch_ex(kern, dim3(p.grid), dim3(kTcThreads), LgCfg::kSmemBytes, s, opts, 2, *P);
+}
+}  // namespace
+
+cudaError_t launch_lateral_group_pair(const LateralGroupPlan& plan, cudaStream_t s,
+                                      LaunchOpts opts) {
+  if (plan.grid <= 0) return cudaSuccess;
+  return plan.dtype == DType::BF16 ? launch_lateral_group_pair_t<__nv_bfloat16>(plan, s, opts)
+                                   : launch_lateral_group_pair_t<__half>(plan, s, opts);
+}
 
 cudaError_t launch_neck(const NeckPlan& plan, cudaStream_t s, LaunchOpts opts) {
   if (plan.grid <= 0) return cudaSuccess;

@@ -391,9 +391,11 @@ RAGGED = [(52, 70), (26, 35), (13, 18), (7, 9)]
     {"grouped_topdown": 1, "ksplit_p5": 4, "ksplit_p4": 2, "ksplit_p3": 2}, {"merge_two_levels": 1},
     {"nsplit_p5": 2, "nsplit_p4": 2, "nsplit_p3": 2}, {"grouped_topdown": 1, "nsplit_p5": 2},
     {"nsplit_p5": 2, "ksplit_p4": 2, "nsplit_p3": 2}, {"p2_lateral_dynamic": 1},
-    {"p2_lateral_dynamic": 1, "p2_lateral_ctas": 37},
+    {"p2_lateral_dynamic": 1, "p2_lateral_ctas": 37}, {"grouped_laterals_pair": 1},
+    {"grouped_laterals_pair": 1, "merge_two_levels": 1},
 ], ids=["split", "fused", "grouped_topdown", "ksplit", "topdown_ksplit", "merge_two_levels",
-        "nsplit", "topdown_nsplit", "nsplit_ksplit", "p2_dynamic", "p2_dynamic_37ctas"])
+        "nsplit", "topdown_nsplit", "nsplit_ksplit", "p2_dynamic", "p2_dynamic_37ctas",
+        "lateral_pairs", "lateral_pairs_two_level"])
 def test_neck_ragged_tile_seams(cuda_device, opts):
     """Every schedule option on ragged maps against the oracle (max-norm and per-element),
     bitwise deterministic, and each image alone equals its slice of the batch."""
@@ -420,7 +422,8 @@ def test_neck_ragged_tile_seams(cuda_device, opts):
 
 @pytest.mark.parametrize("opts", [{"grouped_topdown": 1}, {"ksplit_p5": 4, "ksplit_p4": 2},
                                   {"grouped_topdown": 1, "ksplit_p5": 2, "ksplit_p4": 2, "ksplit_p3": 2},
-                                  {"p2_lateral_dynamic": 1}, {"p2_lateral_ctas": 74}])
+                                  {"p2_lateral_dynamic": 1}, {"p2_lateral_ctas": 74},
+                                  {"grouped_laterals_pair": 1}])
 def test_grouped_launch_options_full_size(cuda_device, opts):
     """The grouped-lateral options at the R50 800x1216 batch-2 workload: the first image
     against the oracle, repeated launches bitwise equal (the split-K sum is order-free and the
@@ -445,20 +448,24 @@ def test_grouped_launch_options_full_size(cuda_device, opts):
     _check([o[:1] for o in outs], ref, torch.bfloat16)
 
 
-def test_channel_half_laterals_equal_whole_tiles_bitwise(cuda_device):
-    """Channel-half units (N = 128 MMAs over 128-row weight boxes) accumulate every output
-    element over the same K order as whole tiles: the neck is bitwise the same with and
-    without them, at the R50 800x1216 batch-2 workload, and matches the oracle."""
+@pytest.mark.parametrize("variant", [{"nsplit_p3": 2, "nsplit_p4": 2, "nsplit_p5": 2},
+                                     {"grouped_laterals_pair": 1}], ids=["nsplit", "pairs"])
+def test_grouped_lateral_variants_equal_whole_tiles_bitwise(cuda_device, variant):
+    """Channel-half units (N = 128 MMAs over 128-row weight boxes) and the CTA-pair launch
+    (M = 256 MMAs, each CTA streaming half of every weight k-block) accumulate every output
+    element over the same K order as the single-CTA grouped launch: the neck is bitwise the
+    same with and without them, at the R50 800x1216 batch-2 workload, and matches the
+    oracle."""
     import unified_fpn as U
     sizes = O.level_sizes(800, 1216)
     host = O.make_features(2, O.R50_CHANNELS, sizes, seed=93)
     wts = O.make_weights(O.R50_CHANNELS, seed=94, bias_scale=0.1)
     xin = [_cl(f.to(torch.bfloat16).cuda()) for f in host]
     res = []
-    for ns in (1, 2):
+    for on in (0, 1):
         fpn = U.UnifiedFPN()
-        for lv in (3, 4, 5):
-            fpn.set_option(f"nsplit_p{lv}", ns)
+        for k, v in (variant.items() if on else ()):
+            fpn.set_option(k, v)
         fpn.initialize_weights(wts.lat_w, wts.lat_b, wts.out_w, wts.out_b)
         res.append([o.clone() for o in _run(fpn, xin)])
         assert fpn.device_status() == 0
