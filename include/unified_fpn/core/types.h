@@ -184,8 +184,10 @@ struct FPNKernelConfig {
   // 3x3 on CTA pairs: run a short last round of pair units as channel halves (N = 128 each).
   bool conv3x3_tail_halves = true;
   // 16-bit split schedule: the grouped raw P5 / P4 / P3 laterals on CTA pairs (each SM
-  // streams half of every weight k-block; host-dealt static schedule).  Same bits.
-  bool grouped_laterals_pair = false;
+  // streams half of every weight k-block; host-dealt static schedule).  Same bits as the
+  // single-CTA grouped launch (false), which split-K, channel halves and top-down adds in
+  // the launch still use.
+  bool grouped_laterals_pair = true;
   // Self-test of the device's bounded waits (0 = off): on the fused schedule, the P2 3x3
   // waits for a lateral tile that never comes, with a limit of this many microseconds, so
   // the forward ends with status kDevTimeoutDependency (outputs undefined) and the engine

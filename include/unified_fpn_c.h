@@ -150,8 +150,9 @@ int ufpn_core_set_schedule_options(ufpn_core* core, int programmatic_launch, int
  *                            unit sums the fp32 partials in a fixed order: deterministic)
  *   "p2_lateral_ctas"  0..4096  CTAs of the 16-bit P2 lateral (0 = one per SM): fewer leave
  *                            SMs to the P3 / P4 3x3s running beside it
- *   "grouped_laterals_pair"  0/1  the grouped raw P5 / P4 / P3 laterals on CTA pairs, each SM
- *                            streaming half of every weight k-block (the same bits)
+ *   "grouped_laterals_pair"  0/1  (default 1) the grouped raw P5 / P4 / P3 laterals on CTA
+ *                            pairs, each SM streaming half of every weight k-block (the same
+ *                            bits as 0, the single-CTA launch)
  *   "conv3x3_tail_halves"  0/1  (default 1) a 3x3 on CTA pairs runs a last round of at most
  *                            half as many units as pairs as channel halves (N = 128), in half
  *                            the time; the same bits

@@ -464,8 +464,9 @@ def test_grouped_lateral_variants_equal_whole_tiles_bitwise(cuda_device, variant
     res = []
     for on in (0, 1):
         fpn = U.UnifiedFPN()
+        fpn.set_option("grouped_laterals_pair", 0)  # the single-CTA grouped launch ...
         for k, v in (variant.items() if on else ()):
-            fpn.set_option(k, v)
+            fpn.set_option(k, v)                    # ... against the variant
         fpn.initialize_weights(wts.lat_w, wts.lat_b, wts.out_w, wts.out_b)
         res.append([o.clone() for o in _run(fpn, xin)])
         assert fpn.device_status() == 0
