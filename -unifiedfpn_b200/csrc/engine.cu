@@ -642,16 +642,16 @@ struct UnifiedFPNCore::Impl {
     auto ns = [&](int l) { return ks(l) == 1 && (l == 3 || !td) ? cfg.lateral_nsplit[l] : 1; };
     const ufpn::NeckJobSpec grouped[3] = {
         {0, 3, 0, ks(3), ns(3)}, {0, 2, td, ks(2), ns(2)}, {0, 1, td, ks(1), ns(1)}};
-    // grouped_laterals_pair: the same raw laterals on CTA pairs (whole tiles only: no top-down
-    // add, split-K or channel halves in the launch; a geometry too large for its static plan
-    // falls back to the single-CTA launch).
+    // grouped_laterals_pair: the same raw laterals on CTA pairs (channel halves per level as
+    // configured; no top-down add or split-K in the launch; a geometry too large for its
+    // static plan falls back to the single-CTA launch).
     bool pair_done = false;
-    if (cfg.grouped_laterals_pair && !td && ks(1) * ks(2) * ks(3) == 1 &&
-        ns(1) * ns(2) * ns(3) == 1) {
+    if (cfg.grouped_laterals_pair && !td && ks(1) * ks(2) * ks(3) == 1) {
       ufpn::LateralGroupPlan lplan;
       const int which[3] = {3, 2, 1};
-      const cudaError_t pe =
-          ufpn::plan_lateral_group_pair(lplan, dtype, batch, lv, which, 3, d_status, 0);
+      const int halves[3] = {ns(3), ns(2), ns(1)};
+      const cudaError_t pe = ufpn::plan_lateral_group_pair(lplan, dtype, batch, lv, which, 3,
+                                                           d_status, 0, halves);
       if (pe == cudaSuccess) {
         ok(ufpn::launch_lateral_group_pair(lplan, main, nchw ? chain : chain_first),
            "grouped laterals (pairs) launch");

@@ -11,6 +11,10 @@
 // 48, so 6 stages fit where 4 did.  The deepest tiles, P5's 32 k-blocks, set the launch's
 // length; on pairs each SM's share of them is both smaller and faster to feed.
 //
+// Channel halves (a job's nsplit = 2): each of its pair units runs as two items of N = 128
+// (M = 256, each CTA staging 64 rows of every weight k-block through map_bh), so a deep
+// unit (P5's 32 k-blocks) holds its pair about half as long; same bits as whole units.
+//
 // Schedule: static, computed on the host (plan_lateral_group_pair): the pair units (two
 // consecutive tiles of one level) are dealt longest first to the least-loaded pair, so the
 // 32-k-block P5 units start first and the short P3 units fill in behind them.  Each pair
@@ -38,8 +42,9 @@ struct LgJob {
   CUtensorMap map_a;    // C_l NHWC, box (64 channels, tile_w, tile_h, 1)
   CUtensorMap map_b;    // weights [256][Cin], box (64, 128 rows): one CTA's half
   CUtensorMap map_out;  // L_l NHWC, box (64, min(tile_w, 32), 32 / that, 1)
+  CUtensorMap map_bh;   // nsplit 2: weights, box (64, 64 rows): one CTA's half of a half
   const float* bias;    // [256]
-  int num_tiles, num_kb;
+  int num_tiles, num_kb, nsplit;
   int N_img, H, W;
   int tile_w, tile_h, tiles_x, tiles_y;
 };
@@ -49,9 +54,10 @@ struct LgParams {
   int num_jobs;
   int num_pairs;
   int* status;
-  // pair p's units: items[off[p] .. off[p + 1]), each (job << 14) | unit (unit u = tiles 2u
-  // and 2u + 1 of that job; a missing second tile is computed on zero-filled input, never
-  // stored)
+  // pair p's items: items[off[p] .. off[p + 1]), each (job << 14) | (part << 12) | unit:
+  // unit u = tiles 2u and 2u + 1 of that job (a missing second tile is computed on
+  // zero-filled input, never stored); part 0 = all 256 output channels, 1 / 2 = channels
+  // 0..127 / 128..255 (N = 128)
   unsigned short off[kLgMaxPairs + 1];
   unsigned short items[kLgMaxItems];
 };
@@ -64,6 +70,10 @@ struct LgCfg {
   static constexpr int kSmemBytes = kOffBars + 256 + 1024;
 };
 static_assert(LgCfg::kSmemBytes <= 232448, "lateral group pair smem");
+
+__device__ __forceinline__ int lg_job(unsigned it) { return static_cast<int>(it >> 14); }
+__device__ __forceinline__ int lg_part(unsigned it) { return static_cast<int>((it >> 12) & 3u); }
+__device__ __forceinline__ int lg_unit(unsigned it) { return static_cast<int>(it & 0xFFFu); }
 
 __device__ __forceinline__ void lg_tile_origin(const LgJob& jb, int tile, int& n, int& x0,
                                                int& y0) {
@@ -120,6 +130,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       prefetch_tmap(&P.jobs[j].map_a);
       prefetch_tmap(&P.jobs[j].map_b);
       prefetch_tmap(&P.jobs[j].map_out);
+      if (P.jobs[j].nsplit > 1) prefetch_tmap(&P.jobs[j].map_bh);
     }
   }
   if (warp == 1) {
@@ -136,25 +147,30 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // ------------------------------------------------------------ TMA producer (each CTA)
     if (lane == 0) {
       const uint32_t full0 = mapa_shared(smem_u32(full_bar), 0);
-      const int brow = static_cast<int>(rank) * (kTcBlockN / 2);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
       for (int i = i0; ok && i < i1; ++i) {
-        const LgJob& jb = P.jobs[P.items[i] >> 14];
-        const int u = P.items[i] & 0x3FFF;
+        const LgJob& jb = P.jobs[lg_job(P.items[i])];
+        const int part = lg_part(P.items[i]);
+        // weight rows this CTA stages per k-block: 128 of 256, or 64 of a half's 128
+        const int brow = part == 0 ? static_cast<int>(rank) * (kTcBlockN / 2)
+                                   : (part - 1) * (kTcBlockN / 2) +
+                                         static_cast<int>(rank) * (kTcBlockN / 4);
+        const CUtensorMap* mb = part == 0 ? &jb.map_b : &jb.map_bh;
+        const uint32_t bytes = 2u * (kTcAStage + (part == 0 ? kPairBStage : kPairBStage / 2));
         int n, x0, y0;
-        lg_tile_origin(jb, 2 * u + static_cast<int>(rank), n, x0, y0);
+        lg_tile_origin(jb, 2 * lg_unit(P.items[i]) + static_cast<int>(rank), n, x0, y0);
         for (int kb = 0; kb < jb.num_kb; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, P.status,
                          kDevTimeoutProducer)) {
             ok = false;
             break;
           }
-          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2u * (kTcAStage + kPairBStage));
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], bytes);
           tma_load_4d_pair(smem_a + stage * kTcAStage, &jb.map_a, full0 + stage * 8u,
                            kb * kTcBlockK, x0, y0, n, kPolicyEvictFirst);
-          tma_load_2d_pair(smem_b + stage * kPairBStage, &jb.map_b, full0 + stage * 8u,
+          tma_load_2d_pair(smem_b + stage * kPairBStage, mb, full0 + stage * 8u,
                            kb * kTcBlockK, brow, kPolicyEvictLast);
           if (++stage == S) {
             stage = 0;
@@ -170,13 +186,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (leader)
     if (leader && lane == 0) {
-      constexpr uint32_t idesc =
+      constexpr uint32_t idesc_full =
           make_idesc(2 * kTcBlockM, kTcBlockN, TcElem<T>::kFmt, TcElem<T>::kFmt);
+      constexpr uint32_t idesc_half =
+          make_idesc(2 * kTcBlockM, kTcBlockN / 2, TcElem<T>::kFmt, TcElem<T>::kFmt);
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
       for (int i = i0; ok && i < i1; ++i) {
-        const int nkb = P.jobs[P.items[i] >> 14].num_kb;
+        const int nkb = P.jobs[lg_job(P.items[i])].num_kb;
+        const uint32_t idesc = lg_part(P.items[i]) == 0 ? idesc_full : idesc_half;
         if (!mbar_wait(&acce_bar[acc], acc_phase ^ 1u, abort_flag, P.status, kDevTimeoutMma))
           break;
         tc_fence_after();
@@ -220,8 +239,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int i = i0; i < i1; ++i) {
-      const LgJob& jb = P.jobs[P.items[i] >> 14];
-      const int tile = 2 * (P.items[i] & 0x3FFF) + static_cast<int>(rank);
+      const LgJob& jb = P.jobs[lg_job(P.items[i])];
+      const int part = lg_part(P.items[i]);
+      const int tile = 2 * lg_unit(P.items[i]) + static_cast<int>(rank);
       const bool real = tile < jb.num_tiles;
       const bool ok =
           mbar_wait(&accf_bar[acc], acc_phase, abort_flag, P.status, kDevTimeoutEpilogue);
@@ -233,10 +253,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const int wrow0 = quarter * 32;
       const int ox = x0 + (wrow0 % tw);
       const int oy = y0 + wrow0 / tw;
+      // a half item's N = 128 accumulator: columns 0..127 of the buffer, 64 per warp
+      const int nsteps = part == 0 ? 2 : 1;
+      const int tcol0 = part == 0 ? chalf * 128 : chalf * 64;
+      const int ocol0 = part == 0 ? tcol0 : (part - 1) * 128 + tcol0;
 #pragma unroll 1
-      for (int step = 0; step < 2; ++step) {
-        const int col0 = chalf * 128 + step * 64;
-        const uint32_t taddr = tmem_base + static_cast<uint32_t>(acc * kTcBlockN + col0) +
+      for (int step = 0; step < nsteps; ++step) {
+        const int col0 = ocol0 + step * 64;  // output channel of the step's first column
+        const uint32_t taddr = tmem_base +
+                               static_cast<uint32_t>(acc * kTcBlockN + tcol0 + step * 64) +
                                (static_cast<uint32_t>(quarter * 32) << 16);
         // both 32-column halves of the step with one wait
         uint32_t r[64];
@@ -245,7 +270,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tmem_ld32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
         if (lane == 0) bulk_wait_group_read<0>();  // the staging buffer's last store read it
         tmem_wait_ld();
-        if (step == 1) {
+        if (step == nsteps - 1) {
           // every accumulator column of this warp is in registers: free the TMEM buffer
           tc_fence_before();
           __syncwarp();
@@ -272,7 +297,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         __syncwarp();
         if (lane == 0) {
           // every use commits a group (empty for the virtual tile past the end)
-          if (real) tma_store_4d(&jb.map_out, smem_stage + ew * kTcStagingPerWarp, col0, ox, oy, n);
+          if (real)
+            tma_store_4d(&jb.map_out, smem_stage + ew * kTcStagingPerWarp, col0, ox, oy, n);
           bulk_commit_group();
         }
       }

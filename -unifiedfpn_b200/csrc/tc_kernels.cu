@@ -761,14 +761,14 @@ static_assert(sizeof(LgParams) <= sizeof(LateralGroupPlan::params),
 
 cudaError_t plan_lateral_group_pair(LateralGroupPlan& plan, DType dt, int N,
                                     const NeckLevel* lv, const int* which, int count,
-                                    int* status, int max_ctas) {
+                                    int* status, int max_ctas, const int* nsplit) {
   if (dt != DType::BF16 && dt != DType::F16) return cudaErrorNotSupported;
   if (N <= 0 || count < 1 || count > kLgMaxJobs || !which) return cudaErrorInvalidValue;
   LgParams* P = reinterpret_cast<LgParams*>(plan.params);
   std::memset(plan.params, 0, sizeof(plan.params));
-  // (job, units, k-blocks per unit)
+  // (job, units, k-blocks per unit, parts per unit)
   struct JobUnits {
-    int job, units, kb;
+    int job, units, kb, parts;
   };
   std::vector<JobUnits> ju;
   long long total_units = 0;
@@ -792,6 +792,8 @@ cudaError_t plan_lateral_group_pair(LateralGroupPlan& plan, DType dt, int N,
     if (tiles >= (1LL << 28)) return cudaErrorNotSupported;
     J.num_tiles = static_cast<int>(tiles);
     J.num_kb = (L.Cin + kTcBlockK - 1) / kTcBlockK;
+    J.nsplit = nsplit ? nsplit[j] : 1;
+    if (J.nsplit != 1 && J.nsplit != 2) return cudaErrorInvalidValue;
     J.bias = L.lat_b;
     cudaError_t e;
     if ((e = encode_nhwc(&J.map_a, dt, L.x, N, L.H, L.W, L.Cin, t.tile_w, t.tile_h)) !=
@@ -799,33 +801,40 @@ cudaError_t plan_lateral_group_pair(LateralGroupPlan& plan, DType dt, int N,
       return e;
     if ((e = encode_weights(&J.map_b, dt, L.lat_w, L.Cin, kTcBlockN / 2)) != cudaSuccess)
       return e;
+    J.map_bh = J.map_b;
+    if (J.nsplit > 1 &&
+        (e = encode_weights(&J.map_bh, dt, L.lat_w, L.Cin, kTcBlockN / 4)) != cudaSuccess)
+      return e;
     const int sw = t.tile_w < 32 ? t.tile_w : 32;
     if ((e = encode_nhwc(&J.map_out, dt, L.merged, N, L.H, L.W, kTcBlockN, sw, 32 / sw)) !=
         cudaSuccess)
       return e;
     const int units = (J.num_tiles + 1) / 2;
-    if (units >= (1 << 14)) return cudaErrorNotSupported;
-    ju.push_back({j, units, J.num_kb});
-    total_units += units;
+    if (units >= (1 << 12)) return cudaErrorNotSupported;
+    ju.push_back({j, units, J.num_kb, J.nsplit});
+    total_units += static_cast<long long>(units) * J.nsplit;
   }
   if (total_units > kLgMaxItems) return cudaErrorNotSupported;
   const int cap = (max_ctas > 0 ? max_ctas : sm_count()) / 2;
   const int pairs = static_cast<int>(std::min<long long>({total_units, cap, kLgMaxPairs}));
   if (pairs <= 0) return cudaErrorInvalidValue;
-  // Longest first to the least-loaded pair (ties: the lowest pair), k-blocks as the load.
-  std::sort(ju.begin(), ju.end(), [](const JobUnits& a, const JobUnits& b) {
-    return a.kb != b.kb ? a.kb > b.kb : a.job < b.job;
+  // Longest first to the least-loaded pair (ties: the lowest pair).  Cost of an item: its
+  // k-blocks, x 0.6 for a channel half (an N = 128 half of a unit measured ~0.6 of it).
+  auto cost = [](const JobUnits& x) { return x.kb * (x.parts > 1 ? 6 : 10); };
+  std::sort(ju.begin(), ju.end(), [&](const JobUnits& a, const JobUnits& b) {
+    return cost(a) != cost(b) ? cost(a) > cost(b) : a.job < b.job;
   });
   std::vector<long long> load(pairs, 0);
   std::vector<std::vector<unsigned short>> lists(pairs);
   for (const JobUnits& x : ju)
-    for (int u = 0; u < x.units; ++u) {
-      int best = 0;
-      for (int p = 1; p < pairs; ++p)
-        if (load[p] < load[best]) best = p;
-      load[best] += x.kb;
-      lists[best].push_back(static_cast<unsigned short>((x.job << 14) | u));
-    }
+    for (int u = 0; u < x.units; ++u)
+      for (int part = x.parts > 1 ? 1 : 0; part <= (x.parts > 1 ? 2 : 0); ++part) {
+        int best = 0;
+        for (int p = 1; p < pairs; ++p)
+          if (load[p] < load[best]) best = p;
+        load[best] += cost(x);
+        lists[best].push_back(static_cast<unsigned short>((x.job << 14) | (part << 12) | u));
+      }
   int k = 0;
   for (int p = 0; p < pairs; ++p) {
     P->off[p] = static_cast<unsigned short>(k);

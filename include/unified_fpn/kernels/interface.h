@@ -293,9 +293,10 @@ cudaError_t plan_neck_jobs(NeckPlan& plan, DType dt, int N, const NeckLevel* lev
 cudaError_t launch_neck(const NeckPlan& plan, cudaStream_t s, LaunchOpts opts = LaunchOpts());
 // The raw laterals (no top-down add) of levels[0..count) in one launch on CTA pairs (two
 // tiles of a level per tcgen05 cta_group::2 MMA stream, each CTA streaming half of every
-// weight k-block), pair units dealt on the host longest first.  Bitwise the same outputs as
-// plan_neck_jobs with those lateral jobs.  cudaErrorNotSupported: not 16-bit, or more pair
-// units than a plan holds (2048).
+// weight k-block), pair units dealt on the host longest first.  nsplit (optional, per
+// entry, 1 or 2): 2 runs that level's units as two N = 128 halves each.  Bitwise the same
+// outputs as plan_neck_jobs with those lateral jobs.  cudaErrorNotSupported: not 16-bit, or
+// more work items than a plan holds (2048; 4095 pair units per level).
 struct LateralGroupPlan {
   alignas(64) unsigned char params[8192];  // opaque outside tc_kernels.cu
   DType dtype = DType::BF16;
@@ -303,7 +304,7 @@ struct LateralGroupPlan {
 };
 cudaError_t plan_lateral_group_pair(LateralGroupPlan& plan, DType dt, int N,
                                     const NeckLevel* levels, const int* which, int count,
-                                    int* status, int max_ctas);
+                                    int* status, int max_ctas, const int* nsplit = nullptr);
 cudaError_t launch_lateral_group_pair(const LateralGroupPlan& plan, cudaStream_t s,
                                       LaunchOpts opts = LaunchOpts());
 // Self-test of the bounded waits: in a planned launch, the 3x3 job of `level` waits for one

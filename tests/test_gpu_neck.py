@@ -393,9 +393,10 @@ RAGGED = [(52, 70), (26, 35), (13, 18), (7, 9)]
     {"nsplit_p5": 2, "ksplit_p4": 2, "nsplit_p3": 2}, {"p2_lateral_dynamic": 1},
     {"p2_lateral_dynamic": 1, "p2_lateral_ctas": 37}, {"grouped_laterals_pair": 1},
     {"grouped_laterals_pair": 1, "merge_two_levels": 1},
+    {"grouped_laterals_pair": 0, "nsplit_p5": 2, "nsplit_p4": 2, "nsplit_p3": 2},
 ], ids=["split", "fused", "grouped_topdown", "ksplit", "topdown_ksplit", "merge_two_levels",
         "nsplit", "topdown_nsplit", "nsplit_ksplit", "p2_dynamic", "p2_dynamic_37ctas",
-        "lateral_pairs", "lateral_pairs_two_level"])
+        "lateral_pairs", "lateral_pairs_two_level", "nsplit_single_cta"])
 def test_neck_ragged_tile_seams(cuda_device, opts):
     """Every schedule option on ragged maps against the oracle (max-norm and per-element),
     bitwise deterministic, and each image alone equals its slice of the batch."""
