@@ -873,11 +873,11 @@ struct UnifiedFPNCore::Impl {
       Conv3x3Tiling t = tiling_for(l);
       if (!t.halo) t = ufpn::halo_pair_tiling();  // e4m3 runs halo tiles only
       // The CTA-pair 3x3 can quantise M_l itself (per image, in shared memory; no quantise
-      // pass, no e4m3 copy of M_l), but its bf16 staging costs two of the eight weight
-      // stages of this weight-feed-bound kernel: measured 240 us against 181 + 43 us for
-      // quantise-then-convolve at the P2 map of the 640x640 batch-16 workload.  Off.
-      constexpr bool kQuantiseInKernel = false;
-      const bool in_kernel = kQuantiseInKernel && t.pair;
+      // pass, no e4m3 copy of M_l; fp8_quantise_in_conv), but its bf16 staging costs two of
+      // the eight weight stages of this weight-feed-bound kernel: measured 240 us against
+      // 181 + 43 us for quantise-then-convolve at the P2 map of the 640x640 batch-16
+      // workload.  Off by default.
+      const bool in_kernel = cfg.fp8_quantise_in_conv && t.pair;
       // (on the main stream the quantisation follows the P2 lateral kernel; on a side stream
       // it follows an event wait)
       if (quantise && !in_kernel)
@@ -1448,6 +1448,7 @@ const std::vector<EngineOption>& engine_options() {
     o.push_back(bool_option<&FPNKernelConfig::lateral_wide_epilogue>("lateral_wide_epilogue"));
     o.push_back(bool_option<&FPNKernelConfig::conv3x3_tail_halves>("conv3x3_tail_halves"));
     o.push_back(bool_option<&FPNKernelConfig::grouped_laterals_pair>("grouped_laterals_pair"));
+    o.push_back(bool_option<&FPNKernelConfig::fp8_quantise_in_conv>("fp8_quantise_in_conv"));
     o.push_back({"p2_parts", [](int v) { return v >= 0 && v <= 8; },
                  [](UnifiedFPNCore::Impl& m, int v) { m.cfg.p2_parts = v; },
                  [](const UnifiedFPNCore::Impl& m) { return m.cfg.p2_parts; }});
@@ -1594,6 +1595,7 @@ std::string UnifiedFPNCore::autotune(const void* const* in, void* const* out, vo
     if (m.batch >= 2) knobs.push_back({"p2_parts", {0, 2, std::min(m.batch, 4)}});
   } else {
     knobs.push_back({"fp8_two_pass_p2", {0, 1}});
+    knobs.push_back({"fp8_quantise_in_conv", {0, 1}});
   }
   knobs.push_back({"merge_units", {0, 2, 4, 8, 16}});
   knobs.push_back({"merge_two_levels", {0, 1}});

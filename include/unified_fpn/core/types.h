@@ -188,6 +188,9 @@ struct FPNKernelConfig {
   // single-CTA grouped launch (false), which split-K, channel halves and top-down adds in
   // the launch still use.
   bool grouped_laterals_pair = true;
+  // e4m3 schedule: the P2 3x3 (CTA pairs) quantises its bf16 input per image in shared
+  // memory instead of a separate quantisation pass over M2 (the same bits).
+  bool fp8_quantise_in_conv = false;
   // Self-test of the device's bounded waits (0 = off): on the fused schedule, the P2 3x3
   // waits for a lateral tile that never comes, with a limit of this many microseconds, so
   // the forward ends with status kDevTimeoutDependency (outputs undefined) and the engine

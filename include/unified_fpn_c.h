@@ -153,6 +153,8 @@ int ufpn_core_set_schedule_options(ufpn_core* core, int programmatic_launch, int
  *   "grouped_laterals_pair"  0/1  (default 1) the grouped raw P5 / P4 / P3 laterals on CTA
  *                            pairs, each SM streaming half of every weight k-block (the same
  *                            bits as 0, the single-CTA launch)
+ *   "fp8_quantise_in_conv"  0/1  e4m3: the P2 3x3 quantises its bf16 input per image in
+ *                            shared memory (no quantisation pass over M2; the same bits)
  *   "conv3x3_tail_halves"  0/1  (default 1) a 3x3 on CTA pairs runs a last round of at most
  *                            half as many units as pairs as channel halves (N = 128), in half
  *                            the time; the same bits
