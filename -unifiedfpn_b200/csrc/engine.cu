@@ -200,6 +200,12 @@ struct UnifiedFPNCore::Impl {
   int merge_units = 0;          // units per block of the merge kernels (0: automatic)
   int p2_lateral_ctas = 0;      // CTAs of the 16-bit P2 lateral (0: one per SM)
   bool p2_lateral_dynamic = false;  // 16-bit P2 lateral as a one-job neck launch (tile claims)
+  // Options set through UnifiedFPNCore::set_option, by name, re-applied after every
+  // (re)configuration so that a choice made before the first forward -- or kept across a new
+  // geometry -- is not replaced by the geometry's defaults.  autotune() drops the entries of
+  // the knobs it tunes (its choice replaces them).
+  std::map<std::string, int> explicit_options;
+  void apply_explicit_options();
   bool profiling = false;
   FPNPerformanceMetrics metrics{};
   struct GraphEntry {
@@ -1069,9 +1075,19 @@ void UnifiedFPNCore::configure_levels(const std::vector<FPNDimensions>& dims, in
   }
   m.p2_pair = false;
   m.merge_units = 0;
-  m.p2_lateral_ctas = 0;
+  // A short P2 lateral (4..10 tiles per SM) on 128 of 148 SMs: the P3 / P4 3x3s then run
+  // beside it instead of waiting for its CTAs (R50 800x1216 x 2, 6.4 tiles per SM: -2.8 %
+  // end to end, same-box A/B).  Longer ones (R50 1024^2 x 8, Swin 1333x800 x 8: 28 tiles per
+  // SM) lose throughput with fewer CTAs, shorter ones (x 1, 3.2) measured no difference.
+  {
+    const long long lt = static_cast<long long>(ufpn::neck_lateral_tiles(N, m.H[0], m.W[0],
+                                                                        m.lat_tiling[0]));
+    const int sms = ufpn::sm_count();
+    m.p2_lateral_ctas = (lt >= 4LL * sms && lt <= 10LL * sms) ? sms * 128 / 148 : 0;
+  }
   m.p2_lateral_dynamic = false;
-  m.apply_tuning_db2();  // a whole-neck tuning of this geometry, if any
+  m.apply_tuning_db2();         // a whole-neck tuning of this geometry, if any
+  m.apply_explicit_options();   // then what the caller chose by name
   const size_t esz = ufpn::dtype_size(dt);
   const size_t msz = dt == DType::E4M3 ? 2 : esz;  // merged maps: bf16 for e4m3 inputs
   size_t total = 0;
@@ -1518,6 +1534,12 @@ void UnifiedFPNCore::set_option(const std::string& name, int value) {
   DeviceGuard g(impl_->device);
   impl_->release_graphs();
   o->set(*impl_, value);
+  impl_->explicit_options[name] = value;
+}
+
+void UnifiedFPNCore::Impl::apply_explicit_options() {
+  for (const auto& kv : explicit_options)
+    if (const EngineOption* o = find_option(kv.first)) o->set(*this, kv.second);
 }
 
 int UnifiedFPNCore::get_option(const std::string& name) const {
@@ -1592,6 +1614,10 @@ std::string UnifiedFPNCore::autotune(const void* const* in, void* const* out, vo
     knobs.push_back({"nsplit_p3", {1, 2}});
     knobs.push_back({"programmatic_launch", {1, 0}});
     knobs.push_back({"lateral_wide_epilogue", {0, 1}});
+    {
+      const int sms = ufpn::sm_count();
+      knobs.push_back({"p2_lateral_ctas", {0, sms * 112 / 148, sms * 128 / 148}});
+    }
     if (m.batch >= 2) knobs.push_back({"p2_parts", {0, 2, std::min(m.batch, 4)}});
   } else {
     knobs.push_back({"fp8_two_pass_p2", {0, 1}});
@@ -1648,6 +1674,7 @@ std::string UnifiedFPNCore::autotune(const void* const* in, void* const* out, vo
   for (const auto& k : knobs) {
     const EngineOption* o = find_option(k.name);
     if (o) chosen[k.name] = o->get(m);
+    m.explicit_options.erase(k.name);  // the tuned choice replaces an explicit one
   }
   m.tuning_db2[m.geometry_key()] = {chosen, best_all};
   for (int l = 0; l < 4; ++l) m.tuning_db[m.tuning_key(l)] = {tiling_code(m.tiling[l]), best_all};

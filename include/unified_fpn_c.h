@@ -149,7 +149,8 @@ int ufpn_core_set_schedule_options(ufpn_core* core, int programmatic_launch, int
  *                       1/2/4 units per lateral tile over K in that launch (a last-arriving
  *                            unit sums the fp32 partials in a fixed order: deterministic)
  *   "p2_lateral_ctas"  0..4096  CTAs of the 16-bit P2 lateral (0 = one per SM): fewer leave
- *                            SMs to the P3 / P4 3x3s running beside it
+ *                            SMs to the P3 / P4 3x3s running beside it.  Default: 128/148 of
+ *                            the SMs when the P2 lateral has 4..10 tiles per SM, else 0
  *   "grouped_laterals_pair"  0/1  (default 1) the grouped raw P5 / P4 / P3 laterals on CTA
  *                            pairs, each SM streaming half of every weight k-block (the same
  *                            bits as 0, the single-CTA launch)

@@ -503,6 +503,31 @@ def test_conv3x3_tail_halves_bitwise_at_full_size(cuda_device, dtype):
     _check([o[:1] for o in res[0]], ref, dtype)
 
 
+def test_options_set_before_the_first_forward_survive_configuration(cuda_device):
+    """Geometry-dependent choices (tilings, the P2 lateral's form, merge blocks) are reset to
+    the geometry's defaults when the engine configures its levels -- at the first forward and
+    at every new geometry.  Values a caller set by name must survive both, and the forward
+    with them must still match the oracle."""
+    import unified_fpn as U
+    chosen = {"p2_lateral_dynamic": 1, "merge_units": 4, "conv3x3_p3": 16, "lateral_tile_p2": 8,
+              "p2_lateral_ctas": 100}
+    fpn = U.UnifiedFPN()
+    for k, v in chosen.items():
+        fpn.set_option(k, v)
+    wts = O.make_weights(O.R50_CHANNELS, seed=99, bias_scale=0.1)
+    fpn.initialize_weights(wts.lat_w, wts.lat_b, wts.out_w, wts.out_b)
+    rw = O.NeckWeights([O.round_to(w, torch.bfloat16) for w in wts.lat_w], wts.lat_b,
+                       [O.round_to(w, torch.bfloat16) for w in wts.out_w], wts.out_b)
+    for sizes in (O.level_sizes(256, 384), RAGGED):  # first forward, then a new geometry
+        host = O.make_features(2, O.R50_CHANNELS, sizes, seed=100, dist="normal")
+        xin = [_cl(f.to(torch.bfloat16).cuda()) for f in host]
+        outs = [o.clone() for o in _run(fpn, xin)]
+        assert fpn.device_status() == 0
+        assert {k: fpn.get_option(k) for k in chosen} == chosen
+        _check(outs, O.fpn_neck([O.round_to(f, torch.bfloat16) for f in host], rw),
+               torch.bfloat16)
+
+
 def test_schedule_option_api_errors(cuda_device):
     import unified_fpn as U
     fpn = U.UnifiedFPN()
