@@ -1618,7 +1618,11 @@ std::string UnifiedFPNCore::autotune(const void* const* in, void* const* out, vo
       const int sms = ufpn::sm_count();
       knobs.push_back({"p2_lateral_ctas", {0, sms * 112 / 148, sms * 128 / 148}});
     }
-    if (m.batch >= 2) knobs.push_back({"p2_parts", {0, 2, std::min(m.batch, 4)}});
+    if (m.batch >= 2) {
+      Knob k{"p2_parts", {0, 2}};
+      if (m.batch >= 3) k.values.push_back(std::min(m.batch, 4));
+      knobs.push_back(k);
+    }
   } else {
     knobs.push_back({"fp8_two_pass_p2", {0, 1}});
     knobs.push_back({"fp8_quantise_in_conv", {0, 1}});
