@@ -139,6 +139,13 @@ int ufpn_core_set_schedule_options(ufpn_core* core, int programmatic_launch, int
  *   "p2_lateral_pair"   0/1  16-bit P2 lateral on CTA pairs with resident weight halves and
  *                            fp32 top-down taps (when Cin <= 256), else one CTA per tile with
  *                            the top-down add as a tensor-core k-block
+ *   "p2_lateral_dynamic"  0/1  16-bit P2 lateral as a one-job fpn_neck_kernel launch: CTAs
+ *                            claim tiles from a counter, top-down taps added in fp32 in the
+ *                            epilogue
+ *   "lateral_wide_epilogue"  0/1  16-bit P2 lateral with 16 epilogue warps and 3 operand stages
+ *                            (the same bits)
+ *   "p2_parts"          0..8  the P2 level (lateral + 3x3) pipelined over this many groups of
+ *                            images (0 / 1: one launch each for the whole batch)
  *   "merge_units"       0..256  8-pixel units per block of the top-down merge kernels (0:
  *                            automatic, one wave of resident blocks)
  *   "fp8_two_pass_p2"   0/1  as ufpn_core_set_fp8_options
