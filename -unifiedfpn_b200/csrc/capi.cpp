@@ -487,12 +487,15 @@ int ufpn_conv3x3_act(int dtype, const void* x, const void* w, const float* bias,
     t.tile_w = tile_w;
     t.tile_h = 128 / tile_w;
     t.halo = false;
-  } else if (tile_w == -1) {
+  } else if (tile_w == -1 || tile_w == -3) {
     t = ufpn::halo_pair_tiling();
-  } else if (tile_w < 0) {
+  } else if (tile_w < -3) {
     return fail(UFPN_ERR_INVALID_ARG,
-                "tile_w must be 0 (halo tiling), -1 (halo tiling on CTA pairs) or 8..128");
+                "tile_w must be 0 (halo tiling), -1 (halo tiling on CTA pairs), -2 / -3 (the "
+                "same on the map's transposed view) or 8..128");
   }
+  t.transposed = tile_w == -2 || tile_w == -3;
+  if (t.transposed && p6) return fail(UFPN_ERR_INVALID_ARG, "transposed view: no fused P6");
   int* status = device_status_word();
   ufpn::TcPlan plan;
   ufpn::TcScales sc;
@@ -1008,12 +1011,16 @@ int ufpn_conv3x3_e4m3(const void* x, const float* x_scale, int x_scale_per_image
   sc.ascale_per_image = x_scale_per_image != 0;
   sc.wscale = w_scales;
   sc.amax_out = amax_out;
-  if (tile_w != 0 && tile_w != -1)
-    return fail(UFPN_ERR_INVALID_ARG, "e4m3 3x3: tile_w must be 0 (halo) or -1 (halo, CTA pairs)");
+  if (tile_w > 0 || tile_w < -3)
+    return fail(UFPN_ERR_INVALID_ARG,
+                "e4m3 3x3: tile_w must be 0 (halo), -1 (halo, CTA pairs) or -2 / -3 (the same "
+                "on the map's transposed view)");
+  ufpn::Conv3x3Tiling t =
+      tile_w == -1 || tile_w == -3 ? ufpn::halo_pair_tiling() : ufpn::halo_tiling();
+  t.transposed = tile_w == -2 || tile_w == -3;
+  if (t.transposed && p6) return fail(UFPN_ERR_INVALID_ARG, "transposed view: no fused P6");
   ufpn::TcPlan plan;
-  cudaError_t e = ufpn::plan_tc_conv3x3(plan, DType::E4M3, x, w, bias, out, p6, N, H, W,
-                                        tile_w == -1 ? ufpn::halo_pair_tiling()
-                                                     : ufpn::halo_tiling(),
+  cudaError_t e = ufpn::plan_tc_conv3x3(plan, DType::E4M3, x, w, bias, out, p6, N, H, W, t,
                                         device_status_word(), 0, sc);
   if (e != cudaSuccess) return cuda_fail(e, "plan e4m3 conv3x3");
   e = ufpn::launch_tc(plan, static_cast<cudaStream_t>(stream));

@@ -96,8 +96,11 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
   uint64_t* done_bar = acce_bar + 2;
   uint64_t* rfull_bar = done_bar + 1;   // kCvt
   uint64_t* rempty_bar = rfull_bar + 1;  // kCvt
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rempty_bar + 1);
+  uint64_t* cfull_bar = rempty_bar + 1;  // claim ring [kClaimRecs]
+  uint64_t* cempty_bar = cfull_bar + kClaimRecs;  // claim ring, the leader's [kClaimRecs]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(cempty_bar + kClaimRecs);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* claim_rec = abort_flag + 1;  // [kClaimRecs]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -108,6 +111,12 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
   const int items = units + args.pair_tail;  // work items (pair_item_unit)
   const int u0 = static_cast<int>(blockIdx.x >> 1);
   const int ustep = static_cast<int>(gridDim.x >> 1);
+  // Dynamic claims: every role but the claimer reads the items from the ring; per CTA the
+  // readers are the epilogue warps, the converter warps and one thread (the MMA issuer in
+  // the leader, the producer in the peer).
+  const bool dyn = args.claim != nullptr;
+  constexpr int kClaimReaders = 2 * (kTcEpiWarps + 1 + (kCvt ? kPairCvtWarps : 0));
+  ClaimRing ring{claim_rec, cfull_bar, mapa_shared(smem_u32(cempty_bar), 0), 0, 0u};
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -125,6 +134,10 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
     mbar_init(done_bar, 1);
     mbar_init(rfull_bar, 1);
     mbar_init(rempty_bar, kPairCvtWarps);
+    for (int r = 0; r < kClaimRecs; ++r) {
+      mbar_init(&cfull_bar[r], 1);
+      mbar_init(&cempty_bar[r], kClaimReaders);
+    }
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tmap(&map_a);
@@ -151,7 +164,37 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
       const uint32_t full0 = mapa_shared(smem_u32(full_bar), 0);
       const uint32_t hfull0 = mapa_shared(smem_u32(hfull_bar), 0);
       uint32_t rphase = 0;
-      for (int it = u0; ok && it < items; it += ustep) {
+      // Dynamic claims (leader): the next item is claimed as the current item's last channel
+      // block starts, so that the atomic's round trip overlaps that block's nine weight loads,
+      // and published once the current item's loads are all issued.
+      int cslot = 0;
+      uint32_t cphase = 0;
+      int pending = 0;
+      auto claim_begin = [&]() -> bool {
+        if (!mbar_wait_acq_cluster(&cempty_bar[cslot], cphase ^ 1u, abort_flag, args.status,
+                                   kDevTimeoutProducer))
+          return false;
+        pending = atomicAdd(args.claim, 1);
+        return true;
+      };
+      auto claim_end = [&](int& item) {
+        item = pending < items ? pending : items;
+        claim_publish(claim_rec, cfull_bar, cslot, item);
+        if (++cslot == kClaimRecs) {
+          cslot = 0;
+          cphase ^= 1u;
+        }
+      };
+      int it = u0;
+      if (dyn) {
+        if (leader) {
+          ok = claim_begin();
+          if (ok) claim_end(it);
+        } else {
+          ok = ring.next(it, abort_flag, args.status, kDevTimeoutProducer);
+        }
+      }
+      for (; ok && it < items;) {
         int half;
         const int u = pair_item_unit(args, units, it, half);
         // weight rows this CTA stages per k-block: 128 of 256, or 64 of a half's 128
@@ -162,6 +205,10 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
         int n, x0, y0;
         tc_tile_origin(args, 2 * u + static_cast<int>(rank), n, x0, y0);
         for (int cb = 0; ok && cb < cin_blocks; ++cb) {
+          if (dyn && leader && cb == cin_blocks - 1 && !claim_begin()) {
+            ok = false;
+            break;
+          }
           if constexpr (kCvt) {
             // bf16 halo (channels cb*128 .. +127 as two 64-channel boxes) for the converter
             if (!mbar_wait(rempty_bar, rphase ^ 1u, abort_flag, args.status,
@@ -203,6 +250,12 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
             }
           }
         }
+        if (!dyn)
+          it += ustep;
+        else if (ok && leader)
+          claim_end(it);
+        else if (ok)
+          ok = ring.next(it, abort_flag, args.status, kDevTimeoutProducer);
       }
       griddep_launch_dependents();  // this CTA's last loads are issued
       // Copies in flight complete on the leader's barriers; after an abort, give them time
@@ -219,7 +272,9 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
       int stage = 0, hb = 0, acc = 0;
       uint32_t phase = 0, hphase = 0, acc_phase = 0;
       bool ok = true;
-      for (int it = u0; ok && it < items; it += ustep) {
+      for (int it = u0;; it += ustep) {
+        if (dyn && !ring.next(it, abort_flag, args.status, kDevTimeoutMma)) break;
+        if (!ok || it >= items) break;
         int half;
         pair_item_unit(args, units, it, half);
         const uint32_t idesc = half < 0 ? idesc_full : idesc_half;
@@ -240,9 +295,8 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
               break;
             }
             tc_fence_after();
-            const int dy = tap / 3, dx = tap % 3;
             const uint64_t adesc = sdesc_kmajor_sw128_stride(
-                halo_addr + static_cast<uint32_t>((dy * (kHaloTileW + 2) + dx) * 128),
+                halo_addr + static_cast<uint32_t>(halo_tap_offset(tap, args.transposed) * 128),
                 (kHaloTileW + 2) * 128);
             const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(smem_b + stage * kPairBStage));
 #pragma unroll
@@ -276,7 +330,8 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
   } else if (warp < 2 + kTcEpiWarps) {
     tc_epilogue<1, T, true>(args, &map_out, tmem_base, accf_bar, acce_bar, smem_stage,
                             abort_flag, warp, lane, false,
-                            mapa_shared(smem_u32(acce_bar), 0));
+                            mapa_shared(smem_u32(acce_bar), 0), nullptr,
+                            dyn ? &ring : nullptr);
   } else if constexpr (kCvt) {
     // ------------------------------------------------------------ converter (each CTA)
     const int ct = threadIdx.x - 32 * (2 + kTcEpiWarps);  // 0 .. 32 * kPairCvtWarps - 1
@@ -285,7 +340,9 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
     int hb = 0;
     uint32_t hphase = 0, rphase = 0;
     bool ok = true;
-    for (int it = u0; ok && it < items; it += ustep) {
+    for (int it = u0;; it += ustep) {
+      if (dyn && !ring.next_warp(it, lane, abort_flag, args.status, kDevTimeoutProducer)) break;
+      if (!ok || it >= items) break;
       int half;
       const int tile = 2 * pair_item_unit(args, units, it, half) + static_cast<int>(rank);
       int n, x0, y0;
@@ -342,6 +399,16 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
     __syncwarp();
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, kTcTmemCols);
+  }
+  if (dyn && threadIdx.x == 0) {
+    // The last CTA to leave (every claim of the launch is made by then) resets the counters
+    // for the next launch.
+    __threadfence();
+    if (atomicAdd(args.claim + 1, 1) == static_cast<int>(gridDim.x) - 1) {
+      args.claim[0] = 0;
+      args.claim[1] = 0;
+      __threadfence();
+    }
   }
 }
 

@@ -446,6 +446,17 @@ struct UnifiedFPNCore::Impl {
     t.tail_halves = cfg.conv3x3_tail_halves;
     return t;
   }
+  // Claim counters of level l's 3x3 (used when it runs on CTA pairs): two ints of the
+  // schedule area per level, zero between launches (device_status(true) clears them after
+  // an abort).
+  int* conv_claim(int l) const { return cfg.conv3x3_dynamic ? d_sched + 32 + 2 * l : nullptr; }
+  // The 3x3 tiling of level l launched on its own: halo tiles on the map's transposed view
+  // where that needs fewer tiles (conv3x3_transpose), except with the fused P6 output.
+  Conv3x3Tiling conv_tiling_for(int l, Conv3x3Tiling t, bool with_p6) const {
+    t.transposed = t.halo && !with_p6 && cfg.conv3x3_transpose &&
+                   ufpn::halo_transpose_pays(H[l], W[l]);
+    return t;
+  }
 
   void check(cudaError_t e, const char* what) {
     if (e != cudaSuccess) FPN_THROW(std::string(what) + ": " + cudaGetErrorString(e));
@@ -626,9 +637,11 @@ struct UnifiedFPNCore::Impl {
         check(cudaStreamWaitEvent(st, ev_lat[l], 0), "event");
       }
       TcPlan conv;
-      check(ufpn::plan_tc_conv3x3(conv, dtype, merged[l], out_wp[l], out_b[l], o[l],
-                                  l == 3 ? o6 : nullptr, batch, H[l], W[l], tiling_for(l),
-                                  d_status, 0, act_scales()),
+      void* const p6_out = l == 3 ? o6 : nullptr;
+      check(ufpn::plan_tc_conv3x3(conv, dtype, merged[l], out_wp[l], out_b[l], o[l], p6_out,
+                                  batch, H[l], W[l],
+                                  conv_tiling_for(l, tiling_for(l), p6_out != nullptr),
+                                  d_status, 0, act_scales(), conv_claim(l)),
             "plan conv3x3");
       // (on the main stream the 3x3 follows a kernel: the P2 lateral, or the previous
       // level's merge / 3x3 when every kernel runs on one stream)
@@ -770,7 +783,8 @@ struct UnifiedFPNCore::Impl {
         TcPlan conv;
         check(ufpn::plan_tc_conv3x3(conv, dtype, static_cast<char*>(merged[0]) + px0 * cout * esz,
                                     out_wp[0], out_b[0], static_cast<char*>(o[0]) + px0 * cout * esz,
-                                    nullptr, n1 - n0, H[0], W[0], tiling_for(0), d_status, 0,
+                                    nullptr, n1 - n0, H[0], W[0],
+                                    conv_tiling_for(0, tiling_for(0), false), d_status, 0,
                                     act_scales()),
               "plan conv3x3");
         ok(ufpn::launch_tc(conv, p2_side), "conv3x3 launch");
@@ -878,6 +892,7 @@ struct UnifiedFPNCore::Impl {
       const long long n = static_cast<long long>(batch) * H[l] * W[l] * cout;
       Conv3x3Tiling t = tiling_for(l);
       if (!t.halo) t = ufpn::halo_pair_tiling();  // e4m3 runs halo tiles only
+      t = conv_tiling_for(l, t, l == 3 && p6 != nullptr);
       // The CTA-pair 3x3 can quantise M_l itself (per image, in shared memory; no quantise
       // pass, no e4m3 copy of M_l; fp8_quantise_in_conv), but its bf16 staging costs two of
       // the eight weight stages of this weight-feed-bound kernel: measured 240 us against
@@ -899,7 +914,7 @@ struct UnifiedFPNCore::Impl {
       TcPlan conv;
       check(ufpn::plan_tc_conv3x3(conv, DType::E4M3, in_kernel ? merged[l] : qmerged[l],
                                   out_wp[l], out_b[l], out[l], l == 3 ? p6 : nullptr, batch,
-                                  H[l], W[l], t, d_status, 0, sc),
+                                  H[l], W[l], t, d_status, 0, sc, conv_claim(l)),
             "plan e4m3 conv3x3");
       ok(ufpn::launch_tc(conv, conv_st,
                          opts(pdl && (conv_st == main || (quantise && !in_kernel)))),
@@ -1463,6 +1478,8 @@ const std::vector<EngineOption>& engine_options() {
     o.push_back(bool_option<&FPNKernelConfig::fp8_two_pass_p2>("fp8_two_pass_p2"));
     o.push_back(bool_option<&FPNKernelConfig::lateral_wide_epilogue>("lateral_wide_epilogue"));
     o.push_back(bool_option<&FPNKernelConfig::conv3x3_tail_halves>("conv3x3_tail_halves"));
+    o.push_back(bool_option<&FPNKernelConfig::conv3x3_transpose>("conv3x3_transpose"));
+    o.push_back(bool_option<&FPNKernelConfig::conv3x3_dynamic>("conv3x3_dynamic"));
     o.push_back(bool_option<&FPNKernelConfig::grouped_laterals_pair>("grouped_laterals_pair"));
     o.push_back(bool_option<&FPNKernelConfig::fp8_quantise_in_conv>("fp8_quantise_in_conv"));
     o.push_back({"p2_parts", [](int v) { return v >= 0 && v <= 8; },
@@ -1627,6 +1644,8 @@ std::string UnifiedFPNCore::autotune(const void* const* in, void* const* out, vo
     knobs.push_back({"fp8_two_pass_p2", {0, 1}});
     knobs.push_back({"fp8_quantise_in_conv", {0, 1}});
   }
+  knobs.push_back({"conv3x3_transpose", {1, 0}});
+  knobs.push_back({"conv3x3_dynamic", {1, 0}});
   knobs.push_back({"merge_units", {0, 2, 4, 8, 16}});
   knobs.push_back({"merge_two_levels", {0, 1}});
   // Each candidate is compared with the incumbent in back-to-back pairs (the GPU's clock,

@@ -116,6 +116,38 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   }
 }
 
+// The same with acquire at cluster scope: for a barrier that a thread of the other CTA of
+// the cluster arrives on (release at cluster scope) after writing this CTA's shared memory.
+__device__ __forceinline__ bool mbar_test_acq_cluster(uint32_t bar_addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar_addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_acq_cluster(uint64_t* bar, uint32_t parity,
+                                                      volatile int* abort_flag, int* status,
+                                                      int code) {
+  const uint32_t a = smem_u32(bar);
+  if (mbar_test_acq_cluster(a, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (mbar_test_acq_cluster(a, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+      *abort_flag = 1;
+      if (status) atomicCAS(status, 0, code);
+      return false;
+    }
+  }
+}
+
 // Teardown wait: ignores the abort flag, shorter limit, never records.
 __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
   const uint32_t a = smem_u32(bar);
@@ -240,6 +272,10 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
                ::: "memory");
+}
+// 32-bit store to a shared::cluster address (possibly the peer CTA's shared memory).
+__device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
 }
 // Arrive on an mbarrier given by its shared::cluster address (possibly the peer CTA's).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {

@@ -174,7 +174,66 @@ struct TcGemmArgs {
   // output channels (N = 128: channels 0..127, then 128..255), so that a last round with
   // fewer units than pairs takes half as long (0 = every unit whole)
   int pair_tail;
+  // halo 3x3 on the map's transposed view (H, W and the tensor maps swapped by the host):
+  // tap (ky, kx) of the weights shifts the halo by (kx, ky) in the view
+  int transposed;
+  // 3x3 on CTA pairs: dynamic item claims.  claim[0] = next work item, claim[1] = CTAs done;
+  // both zero at launch, reset by the last CTA to leave.  Pairs that reach an SM late (other
+  // streams' CTAs still hold it) then take fewer items instead of ending the launch late.
+  // null: static round robin over the pairs.
+  int* claim;
 };
+
+// Work items of a CTA pair claimed at run time: the leader's producer claims each item from
+// the global counter and publishes it to a ring of kClaimRecs records in BOTH CTAs; every
+// other role of either CTA takes the items in order from its own CTA's ring and, once it has
+// read a record, arrives on the leader's empty barrier of that record (release at cluster
+// scope), so that the claimer reuses a slot only after all of them have read it.
+constexpr int kClaimRecs = 4;
+struct ClaimRing {
+  volatile int* rec;  // this CTA's records [kClaimRecs]
+  uint64_t* full;     // this CTA's full barriers [kClaimRecs] (one arrival: the claimer)
+  uint32_t empty0;    // shared::cluster address of the leader's empty barriers
+  int slot;
+  uint32_t phase;
+  __device__ __forceinline__ void advance() {
+    if (++slot == kClaimRecs) {
+      slot = 0;
+      phase ^= 1u;
+    }
+  }
+  // One thread: the next item (false after an abort or a timeout).
+  __device__ __forceinline__ bool next(int& item, volatile int* abort_flag, int* status,
+                                       int code) {
+    if (!mbar_wait_acq_cluster(&full[slot], phase, abort_flag, status, code)) return false;
+    item = rec[slot];
+    mbar_arrive_cluster(empty0 + static_cast<uint32_t>(slot) * 8u);
+    advance();
+    return true;
+  }
+  // A whole warp: every lane reads the record before lane 0 releases it.
+  __device__ __forceinline__ bool next_warp(int& item, int lane, volatile int* abort_flag,
+                                            int* status, int code) {
+    const bool ok = mbar_wait_acq_cluster(&full[slot], phase, abort_flag, status, code);
+    if (!__all_sync(0xffffffffu, ok)) return false;
+    item = rec[slot];
+    __syncwarp();
+    if (lane == 0) mbar_arrive_cluster(empty0 + static_cast<uint32_t>(slot) * 8u);
+    advance();
+    return true;
+  }
+};
+// The claimer (the leader's producer thread): record `item` in slot `slot` of both CTAs'
+// rings, then arrive on both full barriers (release at cluster scope orders the stores).
+__device__ __forceinline__ void claim_publish(volatile int* rec, uint64_t* full, int slot,
+                                              int item) {
+  const uint32_t r = smem_u32(const_cast<int*>(rec) + slot);
+  st_cluster_u32(mapa_shared(r, 1), static_cast<uint32_t>(item));
+  rec[slot] = item;
+  const uint32_t f = smem_u32(&full[slot]);
+  mbar_arrive_cluster(mapa_shared(f, 1));
+  mbar_arrive_cluster(mapa_shared(f, 0));
+}
 
 // Work items of a CTA-pair 3x3: units [0, units - pair_tail) whole (half = -1), then two
 // channel-half items per tail unit.  Returns the item's pair unit.
@@ -416,7 +475,8 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
                                             uint64_t* acce_bar, uint8_t* smem_stage,
                                             volatile int* abort_flag, int warp, int lane,
                                             bool bil_mma, uint32_t leader_acce = 0,
-                                            const float* bias_s = nullptr) {
+                                            const float* bias_s = nullptr,
+                                            ClaimRing* ring = nullptr) {
   using O = typename TcElem<T>::Out;
   constexpr bool kFp8 = TcElem<T>::kFp8;
   // kEpiW / 4 warps share each TMEM lane quarter; each owns kChans output channels,
@@ -439,8 +499,13 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
   const int units = kPair ? (args.num_tiles + 1) / 2 : args.num_tiles;
   const int items = kPair ? units + args.pair_tail : units;
   const int ustep = kPair ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
-  for (int it = kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
-       it < items; it += ustep) {
+  // (kPair with a claim ring: the items in the order the leader claimed them)
+  for (int it = kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);;
+       it += ustep) {
+    if (kPair && ring != nullptr &&
+        !ring->next_warp(it, lane, abort_flag, args.status, kDevTimeoutEpilogue))
+      break;
+    if (it >= items) break;
     int half = -1;  // channel-half item of a CTA-pair 3x3 (its accumulator has N = 128)
     const int u = kPair ? pair_item_unit(args, units, it, half) : it;
     const int tile = kPair ? 2 * u + rank : u;
@@ -915,6 +980,12 @@ __global__ void __launch_bounds__(TcCfgT<kMode, T, kWideEpi>::kThreads, 1)
 constexpr int kHaloTileW = 8;
 constexpr int kHaloTileH = 16;
 constexpr int kHaloRows = (kHaloTileW + 2) * (kHaloTileH + 2);  // 180
+// Halo row offset of weight tap `tap` (ky * 3 + kx).  On the transposed view of a map (rows
+// and columns swapped) the same tap shifts the halo by (kx, ky).
+__device__ __forceinline__ int halo_tap_offset(int tap, int transposed) {
+  const int ky = tap / 3, kx = tap - 3 * (tap / 3);
+  return transposed ? kx * (kHaloTileW + 2) + ky : ky * (kHaloTileW + 2) + kx;
+}
 constexpr int kHaloBytes = ((kHaloRows * 128 + 1023) / 1024) * 1024;
 constexpr int kHaloStages = 4;  // weight stages
 constexpr int kHaloBufs = 2;    // halo buffers
@@ -1081,9 +1152,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               break;
             }
             tc_fence_after();
-            const int dy = tap / 3, dx = tap % 3;
             const uint64_t adesc = sdesc_kmajor_sw128_stride(
-                halo_addr + static_cast<uint32_t>((dy * (kHaloTileW + 2) + dx) * 128),
+                halo_addr + static_cast<uint32_t>(halo_tap_offset(tap, args.transposed) * 128),
                 (kHaloTileW + 2) * 128);
             const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(smem_b + stage * kTcBStage));
 #pragma unroll

@@ -76,14 +76,17 @@ cudaError_t encode(CUtensorMap* map, DType dt, int rank, const void* base, const
 
 // NHWC activation map [N][H][W][C] with a (one 128-byte row of channels, bw, bh, 1) box, or
 // with inner_bytes = 64 a 64-byte row of channels under the 64-byte swizzle (16-byte chunk c
-// of box row r at chunk c ^ ((r >> 1) & 3)).
+// of box row r at chunk c ^ ((r >> 1) & 3)).  transposed: the map's (N, W, H, C) view --
+// coordinate 1 runs down a column (stride W * C), coordinate 2 along a row (stride C), and a
+// box of (bw, bh) covers bw rows of bh columns, stored column by column.
 cudaError_t encode_nhwc(CUtensorMap* map, DType dt, const void* base, int N, int H, int W, int C,
-                        int bw, int bh, int inner_bytes = 128) {
+                        int bw, int bh, int inner_bytes = 128, bool transposed = false) {
   const uint64_t esz = static_cast<uint64_t>(dtype_size(dt));
-  uint64_t dims[4] = {static_cast<uint64_t>(C), static_cast<uint64_t>(W),
-                      static_cast<uint64_t>(H), static_cast<uint64_t>(N)};
-  uint64_t strides[3] = {static_cast<uint64_t>(C) * esz, static_cast<uint64_t>(W) * C * esz,
-                         static_cast<uint64_t>(H) * W * C * esz};
+  const uint64_t pix = static_cast<uint64_t>(C) * esz, row = static_cast<uint64_t>(W) * pix;
+  uint64_t dims[4] = {static_cast<uint64_t>(C), static_cast<uint64_t>(transposed ? H : W),
+                      static_cast<uint64_t>(transposed ? W : H), static_cast<uint64_t>(N)};
+  uint64_t strides[3] = {transposed ? row : pix, transposed ? pix : row,
+                         static_cast<uint64_t>(H) * row};
   uint32_t box[4] = {static_cast<uint32_t>(inner_bytes / esz), static_cast<uint32_t>(bw),
                      static_cast<uint32_t>(bh), 1};
   return encode(map, dt, 4, base, dims, strides, box,
@@ -343,7 +346,7 @@ cudaError_t plan_tc_lateral_pair(TcPlan& plan, DType dt, const void* x, const vo
 cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w,
                             const float* bias, void* out, void* p6, int N, int H, int W,
                             Conv3x3Tiling tiling, int* status, int max_ctas,
-                            const TcScales& sc) {
+                            const TcScales& sc, int* claim) {
   if (dt != DType::BF16 && dt != DType::F16 && dt != DType::E4M3) return cudaErrorInvalidValue;
   const bool fp8 = dt == DType::E4M3;
   const DType odt = fp8 ? DType::BF16 : dt;
@@ -357,9 +360,15 @@ cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w
       (fp8 && !aligned16(sc.wscale)))
     return cudaErrorMisalignedAddress;
   const int C = kTcBlockN;
+  // Transposed view: the kernel sees a W x H map (its tensor maps swap the two axes) and
+  // mirrors each tap; only halo tilings, and not with the fused P6 (whose indexing is the
+  // map's own).
+  const bool tr = tiling.transposed;
+  if (tr && (!tiling.halo || p6 != nullptr)) return cudaErrorInvalidValue;
   TcGemmArgs a;
   std::memset(&a, 0, sizeof(a));
-  fill_tiling(a, N, H, W, tiling);
+  fill_tiling(a, N, tr ? W : H, tr ? H : W, tiling);
+  a.transposed = tr ? 1 : 0;
   const long long tiles = static_cast<long long>(a.tiles_x) * a.tiles_y * N;
   if (tiles >= (1LL << 31)) return cudaErrorInvalidValue;
   a.num_tiles = static_cast<int>(tiles);
@@ -385,14 +394,15 @@ cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w
   // Halo path: one (tile_w + 2) x (tile_h + 2) box per channel block, origin (-1, -1)
   // (bf16 boxes of 64 channels when the kernel quantises its input itself).
   cudaError_t e = halo ? encode_nhwc(&plan.map_a, cvt ? DType::BF16 : dt, x, N, H, W, C,
-                                     kHaloTileW + 2, kHaloTileH + 2)
+                                     kHaloTileW + 2, kHaloTileH + 2, 128, tr)
                        : encode_nhwc(&plan.map_a, dt, x, N, H, W, C, tiling.tile_w, tiling.tile_h);
   if (e != cudaSuccess) return e;
   if ((e = encode_weights(&plan.map_b, dt, w, 9 * C, tiling.pair ? kTcBlockN / 2 : kTcBlockN)) !=
       cudaSuccess)
     return e;
   const int sw = tiling.tile_w < 32 ? tiling.tile_w : 32;
-  if ((e = encode_nhwc(&plan.map_out, odt, out, N, H, W, kTcBlockN, sw, 32 / sw)) != cudaSuccess)
+  if ((e = encode_nhwc(&plan.map_out, odt, out, N, H, W, kTcBlockN, sw, 32 / sw, 128, tr)) !=
+      cudaSuccess)
     return e;
   plan.map_coarse = plan.map_out;
   plan.mode = cvt ? 4 : (tiling.pair ? 3 : (halo ? 2 : 1));
@@ -400,6 +410,7 @@ cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w
   plan.num_tiles = a.num_tiles;
   const int cap = max_ctas > 0 ? max_ctas : sm_count();
   if (tiling.pair) {
+    a.claim = claim;
     // One (2,1,1) cluster per pair unit (two tiles), at most one CTA per SM.
     const int units = (a.num_tiles + 1) / 2;
     const int clusters = units < cap / 2 ? units : cap / 2;

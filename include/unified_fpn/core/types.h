@@ -183,6 +183,15 @@ struct FPNKernelConfig {
   int lateral_nsplit[4] = {1, 1, 1, 1};
   // 3x3 on CTA pairs: run a short last round of pair units as channel halves (N = 128 each).
   bool conv3x3_tail_halves = true;
+  // Halo 3x3s on the map's transposed view (tiles of 16 columns x 8 rows) wherever that
+  // needs fewer tiles (200 x 304: 475 instead of 494 per image).  The same bits.
+  bool conv3x3_transpose = true;
+  // 3x3s on CTA pairs claim their work items at run time (a device counter) instead of a
+  // static round robin, so that pairs that reach an SM late, while other streams' CTAs hold
+  // it, take fewer items.  Each item's results do not depend on which pair runs it.
+  // Measured slower at R50 800x1216 x 2 (equal-sized items claimed greedily end less evenly
+  // than the static deal's 6.5 rounds): off.
+  bool conv3x3_dynamic = false;
   // 16-bit split schedule: the grouped raw P5 / P4 / P3 laterals on CTA pairs (each SM
   // streams half of every weight k-block; host-dealt static schedule).  Same bits as the
   // single-CTA grouped launch (false), which split-K, channel halves and top-down adds in

@@ -116,6 +116,12 @@ struct Conv3x3Tiling {
   // CTA pairs: a last round with at most half as many units as pairs runs each of its
   // units as two halves over the output channels (N = 128), in half the time (same bits).
   bool tail_halves = true;
+  // Halo tiles only: run the conv on the map's transposed view (rows and columns swapped in
+  // the tensor maps, taps mirrored), so that a tile covers 16 columns x 8 rows.  Maps whose
+  // height is not a multiple of 16 but whose width is (200 x 304) then tile without padded
+  // rows.  Each output element accumulates the same k-blocks in the same order: the results
+  // are bitwise those of the untransposed conv.  Not with a fused P6 output.
+  bool transposed = false;
 };
 // The 3x3 default: halo reuse with 8 x 16 tiles.
 inline Conv3x3Tiling halo_tiling() {
@@ -124,6 +130,12 @@ inline Conv3x3Tiling halo_tiling() {
   t.tile_h = 16;
   t.halo = true;
   return t;
+}
+// Whether an H x W map needs fewer 8 x 16 halo tiles on its transposed view.
+inline bool halo_transpose_pays(int H, int W) {
+  const long long plain = static_cast<long long>((W + 7) / 8) * ((H + 15) / 16);
+  const long long trans = static_cast<long long>((H + 7) / 8) * ((W + 15) / 16);
+  return trans < plain;
 }
 inline Conv3x3Tiling halo_pair_tiling() {
   Conv3x3Tiling t = halo_tiling();
@@ -194,10 +206,13 @@ cudaError_t plan_tc_lateral_pair(TcPlan& plan, DType dt, const void* x, const vo
                                  const float* bias, const void* coarse, void* out, int N,
                                  int Cin, int H, int W, int Hc, int Wc, Conv3x3Tiling tiling,
                                  int* status, int max_ctas = 0);
+// claim (CTA-pair tilings only; else ignored): two device ints, zero before the first launch,
+// through which the pairs claim their work items at run time (the launch leaves them zero
+// again); null = static round robin.  At most one launch in flight per claim pair.
 cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w,
                             const float* bias, void* out, void* p6, int N, int H, int W,
                             Conv3x3Tiling tiling, int* status, int max_ctas,
-                            const TcScales& scales = TcScales());
+                            const TcScales& scales = TcScales(), int* claim = nullptr);
 // Precomputed bilinear-weight table of the lateral's tensor-core top-down add (one 16 KB
 // entry per tile position of an H x W map upsampled from Hc x Wc with tiling t; the same
 // for every image).  Bytes needed (0 when that lateral adds the taps in its epilogue),

@@ -166,6 +166,12 @@ int ufpn_core_set_schedule_options(ufpn_core* core, int programmatic_launch, int
  *   "conv3x3_tail_halves"  0/1  (default 1) a 3x3 on CTA pairs runs a last round of at most
  *                            half as many units as pairs as channel halves (N = 128), in half
  *                            the time; the same bits
+ *   "conv3x3_transpose"  0/1  (default 1) halo 3x3s run on the map's transposed view (16 x 8
+ *                            tiles) where that needs fewer tiles (200 x 304: 475 instead of
+ *                            494 per image); the same bits
+ *   "conv3x3_dynamic"    0/1  (default 0) 3x3s on CTA pairs claim their work items at run
+ *                            time (a device counter) instead of a static round robin; the
+ *                            same bits
  *   "nsplit_p3", "nsplit_p4", "nsplit_p5"
  *                         1/2  units per lateral tile over the output channels in that
  *                            launch (two N = 128 halves: half the weight stream per unit, the
@@ -244,8 +250,10 @@ int ufpn_lateral_conv_pair(int dtype, const void* x, const void* w, const float*
  *   dtype F32: NCHW x, w fp32 [256][256][3][3].
  * tile_w: 0 = 8 x 16 tiles with halo reuse (default: each 64-channel halo is loaded once
  * and shared by the nine taps); -1 = the same tiles on CTA pairs (tcgen05 cta_group::2:
- * two SMs share one M = 256 MMA stream and each streams half of the weights); 8..128 =
- * plain tiles of that width (one box per tap). */
+ * two SMs share one M = 256 MMA stream and each streams half of the weights); -2 / -3 =
+ * 0 / -1 on the map's transposed view (tiles of 16 columns x 8 rows: fewer tiles where H is
+ * not a multiple of 16 but W is; the same bits; no P6); 8..128 = plain tiles of that width
+ * (one box per tap). */
 int ufpn_conv3x3(int dtype, const void* x, const void* w, const float* bias, void* out,
                  void* p6, int N, int H, int W, int tile_w, void* stream);
 /* ufpn_conv3x3 with an output activation fused into its epilogue after the bias (P6, if
@@ -417,8 +425,8 @@ int ufpn_lateral_conv_e4m3(const void* x, const float* x_scale, int x_scale_per_
                            const void* w, const float* w_scales, const float* bias,
                            const void* coarse, void* out, int N, int Cin, int H, int W, int Hc,
                            int Wc, unsigned* amax_out, void* stream);
-/* FP8 3x3 pad-1 conv 256 -> 256 (8 x 16 halo tiles; tile_w -1: on CTA pairs, as for
- * ufpn_conv3x3), NHWC: x e4m3 [N][H][W][256] with device
+/* FP8 3x3 pad-1 conv 256 -> 256 (8 x 16 halo tiles; tile_w -1: on CTA pairs, -2 / -3: the
+ * map's transposed view, as for ufpn_conv3x3), NHWC: x e4m3 [N][H][W][256] with device
  * scale(s) as above; w e4m3 packed [256][9][256] (ufpn_quantize_e4m3_rows with pack_cin =
  * 256) with scales [256]; out (and optional p6 = out[::2, ::2]) bf16; amax_out as above.
  * Same role as launch_output_conv (fpn_engine.cu:315-362). */

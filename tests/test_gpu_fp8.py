@@ -141,6 +141,24 @@ def test_conv3x3_fp8_matches_oracle(cuda_device, shape, per_image):
     assert torch.equal(p6.cpu(), out[:, :, ::2, ::2].cpu())
 
 
+@pytest.mark.parametrize("shape", [(3, 13, 21), (2, 37, 50), (1, 200, 304)])
+def test_conv3x3_fp8_transposed_view_equals_plain(cuda_device, shape):
+    """e4m3 3x3 halo tiles on the map's transposed view (tile_w -2, and -3 on CTA pairs) give
+    bitwise the plain halo tiles' results."""
+    import unified_fpn as U
+    N, H, W = shape
+    g = torch.Generator(device="cuda").manual_seed(16)
+    m = _cl(torch.randn(N, 256, H, W, device="cuda", generator=g).to(torch.bfloat16))
+    w3 = torch.randn(256, 256, 3, 3, device="cuda", generator=g) * (2.0 / 2304) ** 0.5
+    b = (torch.rand(256, device="cuda", generator=g) * 2 - 1) * 0.1
+    qw, sw = U.quantize_fp8_rows(w3, pack3x3=True)
+    qm, sm = U.quantize_fp8(m, per_image=True)
+    ys = [U.fpn_conv3x3_fp8(qm, sm, qw, sw, b, tile_w=t) for t in (0, -2, -1, -3)]
+    torch.cuda.synchronize()
+    assert U.device_status() == 0
+    assert all(torch.equal(ys[0], y) for y in ys[1:])
+
+
 @pytest.mark.parametrize("shape", [(2, 40, 56), (1, 25, 38), (3, 13, 21), (16, 160, 160),
                                    (1, 200, 304)])
 def test_conv3x3_fp8_in_kernel_quantisation(cuda_device, shape):
@@ -282,6 +300,31 @@ def test_fp8_two_pass_p2_lateral_is_bitwise_equal(cuda_device, geom):
         _, _, outs[two_pass] = _run_fp8_neck(chans, wts, qf, sc, fpn=fpn)
     for a, b in zip(outs[False], outs[True]):
         assert torch.equal(a, b)
+
+
+def test_fp8_neck_transposed_view_and_claims_are_bitwise_equal(cuda_device):
+    """e4m3 neck at the Swin 1333x800 level sizes, whose 3x3s tile the P2 / P3 / P4 maps on
+    their transposed views by default (143 instead of 147 tiles at 100 x 167): bitwise what
+    plain tiles give, and what CTA-pair 3x3s that claim their items at run time give, with the
+    separate quantisation pass and with the 3x3 that quantises its input itself, repeated
+    launches included (the claim counters reset themselves)."""
+    import unified_fpn as U
+    chans, sizes = O.SWIN_CHANNELS, [(100, 167), (50, 84), (25, 42), (13, 21)]
+    _, wts, qf, sc = _fp8_case(2, chans, sizes, seed=43)
+    outs = []
+    for opts in ({}, {"conv3x3_transpose": 0}, {"conv3x3_dynamic": 1},
+                 {"fp8_quantise_in_conv": 1}, {"fp8_quantise_in_conv": 1, "conv3x3_dynamic": 1}):
+        fpn = U.UnifiedFPN()
+        for k, v in opts.items():
+            fpn.set_option(k, v)
+        fpn, xin, o = _run_fp8_neck(chans, wts, qf, sc, fpn=fpn)
+        outs.append(o)
+        again = fpn(xin, return_p6=True, input_scales=[float(s) for s in sc])
+        torch.cuda.synchronize()
+        assert fpn.device_status() == 0
+        assert all(torch.equal(a, b) for a, b in zip(o, again))
+    for r in outs[1:]:
+        assert all(torch.equal(a, b) for a, b in zip(outs[0], r))
 
 
 @pytest.mark.parametrize("fp8_in", [False, True])

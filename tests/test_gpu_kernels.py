@@ -274,8 +274,9 @@ def test_conv3x3_cta_pair_equals_single(cuda_device, dtype, shape):
     CTA streaming half of the weights) give bitwise the results of single-CTA halo tiles:
     every output's K summation runs in the same order.  Odd tile counts exercise the
     virtual (never stored) second tile of the last pair; (2, 200, 304) is the R50 P2 map.
-    On 148 SMs (74 pairs) the two 200x304 maps end with a short round (475 units: 31 left,
-    247: 25) that runs as channel halves (N = 128 items)."""
+    On 148 SMs (74 pairs) the 1 x 200 x 304 map ends with a short round (247 units: 25 left)
+    that runs as channel halves (N = 128 items); 2 x 200 x 304 (494 units: 50 left) does
+    not."""
     import unified_fpn as U
     n, h, w_ = shape
     g = torch.Generator().manual_seed(h * 31 + w_)
@@ -292,6 +293,54 @@ def test_conv3x3_cta_pair_equals_single(cuda_device, dtype, shape):
     if n * h * w_ <= 4096:
         ref = O.conv3x3(x.float(), w.to(dtype).float(), b)
         O.check_close(y2.cpu(), ref, dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", [(1, 16, 8), (1, 8, 16), (1, 13, 21), (3, 17, 5), (1, 1, 1),
+                                   (2, 37, 50), (1, 200, 334), (2, 200, 304)])
+def test_conv3x3_transposed_view_equals_plain(cuda_device, dtype, shape):
+    """Halo tiles on the map's transposed view (tile_w -2 on single CTAs, -3 on CTA pairs:
+    16 columns x 8 rows per tile through tensor maps with the two axes swapped, each tap's
+    halo shift mirrored) give bitwise the results of the plain halo tiles, and match the
+    oracle.  Ragged edges fall on the other axis than with plain tiles.  (2, 200, 304), the
+    R50 P2 map: 950 tiles instead of 988, i.e. 475 pair units on 74 pairs whose last 31 run
+    as channel halves."""
+    import unified_fpn as U
+    n, h, w_ = shape
+    g = torch.Generator().manual_seed(h * 37 + w_)
+    x = torch.randn(n, 256, h, w_, generator=g).to(dtype)
+    w = torch.randn(256, 256, 3, 3, generator=g) * (2.0 / 2304) ** 0.5
+    b = torch.rand(256, generator=g) * 0.2 - 0.1
+    xd = _cl(x.to(cuda_device))
+    wp = U.pack_conv3x3_weight(w.to(cuda_device), dtype)
+    bd = b.to(cuda_device)
+    ys = [U.fpn_conv3x3(xd, wp, bd, tile_w=t) for t in (0, -2, -1, -3)]
+    torch.cuda.synchronize()
+    assert U.device_status() == 0
+    assert all(torch.equal(ys[0], y) for y in ys[1:])
+    if n * h * w_ <= 4096:
+        ref = O.conv3x3(x.float(), w.to(dtype).float(), b)
+        O.check_close(ys[1].cpu(), ref, dtype)
+    else:  # first and last image rows of the large maps against the oracle
+        ref = O.conv3x3(x[:1, :, :12].float(), w.to(dtype).float(), b)
+        O.check_close(ys[3][:1, :, :11].cpu(), ref[:, :, :11], dtype)
+        ref = O.conv3x3(x[-1:, :, -12:].float(), w.to(dtype).float(), b)
+        O.check_close(ys[3][-1:, :, -11:].cpu(), ref[:, :, -11:], dtype)
+
+
+def test_conv3x3_transposed_view_refuses_p6(cuda_device):
+    """The fused P6 output indexes the map's own rows: the transposed view refuses it on the
+    host (no launch)."""
+    import unified_fpn as U
+    x = _cl(torch.randn(1, 256, 8, 8, device=cuda_device).to(torch.bfloat16))
+    w = U.pack_conv3x3_weight(torch.randn(256, 256, 3, 3, device=cuda_device), torch.bfloat16)
+    b = torch.zeros(256, device=cuda_device)
+    for t in (-2, -3):
+        with pytest.raises(Exception):
+            U.fpn_conv3x3(x, w, b, p6=True, tile_w=t)
+    with pytest.raises(Exception):
+        U.fpn_conv3x3(x, w, b, tile_w=-4)
+    assert U.device_status() == 0
 
 
 def test_conv3x3_fp32(cuda_device):

@@ -394,9 +394,13 @@ RAGGED = [(52, 70), (26, 35), (13, 18), (7, 9)]
     {"p2_lateral_dynamic": 1, "p2_lateral_ctas": 37}, {"grouped_laterals_pair": 1},
     {"grouped_laterals_pair": 1, "merge_two_levels": 1},
     {"grouped_laterals_pair": 0, "nsplit_p5": 2, "nsplit_p4": 2, "nsplit_p3": 2},
+    {"conv3x3_dynamic": 1}, {"conv3x3_transpose": 0},
+    {"conv3x3_p3": -1, "conv3x3_p4": -1, "conv3x3_p5": -1},
+    {"conv3x3_p3": -1, "conv3x3_p4": -1, "conv3x3_p5": -1, "conv3x3_dynamic": 1},
 ], ids=["split", "fused", "grouped_topdown", "ksplit", "topdown_ksplit", "merge_two_levels",
         "nsplit", "topdown_nsplit", "nsplit_ksplit", "p2_dynamic", "p2_dynamic_37ctas",
-        "lateral_pairs", "lateral_pairs_two_level", "nsplit_single_cta"])
+        "lateral_pairs", "lateral_pairs_two_level", "nsplit_single_cta", "conv_claims",
+        "conv_plain_view", "conv_pairs_all_levels", "conv_pairs_all_levels_claims"])
 def test_neck_ragged_tile_seams(cuda_device, opts):
     """Every schedule option on ragged maps against the oracle (max-norm and per-element),
     bitwise deterministic, and each image alone equals its slice of the batch."""
@@ -480,23 +484,29 @@ def test_grouped_lateral_variants_equal_whole_tiles_bitwise(cuda_device, variant
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_conv3x3_tail_halves_bitwise_at_full_size(cuda_device, dtype):
-    """The P2 3x3 on CTA pairs at the R50 800x1216 batch-2 workload ends with 31 of 475 pair
-    units on 74 pairs; run as channel halves (the default) the neck is bitwise what whole
-    units give (conv3x3_tail_halves=0), and matches the oracle."""
+    """At the R50 800x1216 batch-2 workload the 3x3s tile the P2 / P3 / P4 maps on their
+    transposed views (conv3x3_transpose, the default: 950 / 260 / 70 tiles instead of 988 /
+    266 / 80), and the P2 3x3 on CTA pairs then ends with 31 of 475 pair units on 74 pairs,
+    run as channel halves (conv3x3_tail_halves, the default).  The neck is bitwise what plain
+    tiles, whole units and run-time item claims (conv3x3_dynamic) give, and matches the
+    oracle."""
     import unified_fpn as U
     sizes = O.level_sizes(800, 1216)
     host = O.make_features(2, O.R50_CHANNELS, sizes, seed=95)
     wts = O.make_weights(O.R50_CHANNELS, seed=96, bias_scale=0.1)
     xin = [_cl(f.to(dtype).cuda()) for f in host]
     res = []
-    for on in (1, 0):
+    for opts in ({}, {"conv3x3_tail_halves": 0}, {"conv3x3_transpose": 0},
+                 {"conv3x3_tail_halves": 0, "conv3x3_transpose": 0}, {"conv3x3_dynamic": 1}):
         fpn = U.UnifiedFPN()
-        fpn.set_option("conv3x3_tail_halves", on)
-        assert fpn.get_option("conv3x3_tail_halves") == on
+        for k, v in opts.items():
+            fpn.set_option(k, v)
+            assert fpn.get_option(k) == v
         fpn.initialize_weights(wts.lat_w, wts.lat_b, wts.out_w, wts.out_b)
         res.append([o.clone() for o in _run(fpn, xin)])
         assert fpn.device_status() == 0
-    assert all(torch.equal(a, b) for a, b in zip(*res))
+    for r in res[1:]:
+        assert all(torch.equal(a, b) for a, b in zip(res[0], r))
     rw = O.NeckWeights([O.round_to(w, dtype) for w in wts.lat_w], wts.lat_b,
                        [O.round_to(w, dtype) for w in wts.out_w], wts.out_b)
     ref = O.fpn_neck([O.round_to(f[:1], dtype) for f in host], rw)
