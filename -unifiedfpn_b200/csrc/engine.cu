@@ -197,7 +197,7 @@ struct UnifiedFPNCore::Impl {
   Conv3x3Tiling lat_tiling[4];  // lateral tile shape per level (tuned or the least padding)
   int wb_tile_w = 0;            // lateral tile width the Wb table was built for
   bool p2_pair = false;         // 16-bit P2 lateral on CTA pairs (resident weight halves)
-  int merge_units = 0;          // units per block of the merge kernels (0: automatic)
+  int merge_units = 0;  // merge kernel form / units per block (launch_upsample_add)
   int p2_lateral_ctas = 0;      // CTAs of the 16-bit P2 lateral (0: one per SM)
   bool p2_lateral_dynamic = false;  // 16-bit P2 lateral as a one-job neck launch (tile claims)
   // Options set through UnifiedFPNCore::set_option, by name, re-applied after every
@@ -755,9 +755,11 @@ struct UnifiedFPNCore::Impl {
                   : cudaErrorNotSupported;
       if (pe != cudaSuccess) {
         if (pe != cudaErrorNotSupported) check(pe, "plan lateral pair");
+        ufpn::TcScales lsc;
+        lsc.direct_store = cfg.lateral_direct_store;
         check(ufpn::plan_tc_lateral(lat2, dtype, xin, lat_wp[0], lat_b[0], m3, m2, nb, cin[0],
                                     H[0], W[0], H[1], W[1], lv[0].lat_tiling, d_status,
-                                    p2_lateral_ctas),
+                                    p2_lateral_ctas, lsc),
               "plan lateral");
         ufpn::tc_attach_wb_table(lat2, wb_table);
         if (cfg.lateral_wide_epilogue) ufpn::tc_use_wide_epilogue(lat2);
@@ -1480,6 +1482,7 @@ const std::vector<EngineOption>& engine_options() {
     o.push_back(bool_option<&FPNKernelConfig::conv3x3_tail_halves>("conv3x3_tail_halves"));
     o.push_back(bool_option<&FPNKernelConfig::conv3x3_transpose>("conv3x3_transpose"));
     o.push_back(bool_option<&FPNKernelConfig::conv3x3_dynamic>("conv3x3_dynamic"));
+    o.push_back(bool_option<&FPNKernelConfig::lateral_direct_store>("lateral_direct_store"));
     o.push_back(bool_option<&FPNKernelConfig::grouped_laterals_pair>("grouped_laterals_pair"));
     o.push_back(bool_option<&FPNKernelConfig::fp8_quantise_in_conv>("fp8_quantise_in_conv"));
     o.push_back({"p2_parts", [](int v) { return v >= 0 && v <= 8; },
@@ -1518,7 +1521,7 @@ const std::vector<EngineOption>& engine_options() {
     o.push_back({"p2_lateral_ctas", [](int v) { return v >= 0 && v <= 4096; },
                  [](UnifiedFPNCore::Impl& m, int v) { m.p2_lateral_ctas = v; },
                  [](const UnifiedFPNCore::Impl& m) { return m.p2_lateral_ctas; }});
-    o.push_back({"merge_units", [](int v) { return v >= 0 && v <= 256; },
+    o.push_back({"merge_units", [](int v) { return v >= -1 && v <= 256; },
                  [](UnifiedFPNCore::Impl& m, int v) { m.merge_units = v; },
                  [](const UnifiedFPNCore::Impl& m) { return m.merge_units; }});
     o.push_back({"test_stall_dependency_us", [](int v) { return v >= 0 && v <= 1000000; },
@@ -1631,6 +1634,7 @@ std::string UnifiedFPNCore::autotune(const void* const* in, void* const* out, vo
     knobs.push_back({"nsplit_p3", {1, 2}});
     knobs.push_back({"programmatic_launch", {1, 0}});
     knobs.push_back({"lateral_wide_epilogue", {0, 1}});
+    knobs.push_back({"lateral_direct_store", {0, 1}});
     {
       const int sms = ufpn::sm_count();
       knobs.push_back({"p2_lateral_ctas", {0, sms * 112 / 148, sms * 128 / 148}});
@@ -1646,7 +1650,7 @@ std::string UnifiedFPNCore::autotune(const void* const* in, void* const* out, vo
   }
   knobs.push_back({"conv3x3_transpose", {1, 0}});
   knobs.push_back({"conv3x3_dynamic", {1, 0}});
-  knobs.push_back({"merge_units", {0, 2, 4, 8, 16}});
+  knobs.push_back({"merge_units", {0, -1, 2, 4, 8, 16}});
   knobs.push_back({"merge_two_levels", {0, 1}});
   // Each candidate is compared with the incumbent in back-to-back pairs (the GPU's clock,
   // which drifts over seconds under a power cap, is the same within a pair); it replaces the

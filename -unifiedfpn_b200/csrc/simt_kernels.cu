@@ -370,6 +370,129 @@ __global__ void __launch_bounds__(256, 3) upsample_add_px512_kernel(
 // 800x1216 batch 2, the same on e4m3 640x640 batch 16.
 constexpr int kPx512Batch = 2;
 
+// Unit-per-warp form of the same merge, for maps that upsample along x (Wc / W <= 4 / 7): a
+// warp owns a unit of 8 consecutive output pixels of one row.  It loads the unit's 8 lateral
+// vectors into registers and the unit's coarse window -- 2 rows x kWinCols columns, which hold
+// the taps of all 8 pixels -- into its own slice of shared memory with cp.async (each lane
+// copies, and later reads, only its own 16 bytes of every pixel: no barrier), then computes
+// the 8 pixels from there.  One load round trip per unit and 8 + 2 kWinCols loads of 16 bytes
+// per lane, where one warp per pixel (above) makes 5 per pixel in several dependent rounds.
+// The same fp32 chain per element as upsample_add_px512_kernel: bitwise the same output.  A
+// tap outside the window (a larger ratio, or rounding at its edge) is read from global
+// memory.  Warps take units with a grid stride, so the resident warps work on one band of
+// rows at a time.
+constexpr int kWinCols = 6;
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)),
+               "l"(gmem_src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+template <typename T>
+__global__ void __launch_bounds__(256) upsample_add_unit_kernel(
+    const T* __restrict__ coarse, const T* lat, T* out, int N, int Hc, int Wc, int H, int W,
+    int chunks, float sy_scale, float sx_scale, int ac, unsigned* amax, T* out_s,
+    const float* scale_a, const float* scale_w) {
+  static_assert(sizeof(T) == 2, "16-bit types");
+  griddep_wait();  // (programmatic launch) inputs written by the previous kernel
+  griddep_launch_dependents();
+  __shared__ uint4 win[8][2 * kWinCols][32];  // per warp: row 0 columns, row 1 columns x lanes
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float inv[8];
+  if (out_s) {
+    const float sa = __ldg(scale_a);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) inv[e] = __frcp_rn(sa * __ldg(scale_w + lane * 8 + e));
+  }
+  unsigned m = 0;
+  int m_img = -1;  // image the running maximum m belongs to (warp-uniform)
+  const int total = N * H * chunks;  // < 2^31 (host)
+  for (int u = blockIdx.x * 8 + warp; u < total; u += gridDim.x * 8) {
+    const int r = u / chunks;  // output row over all images
+    const int xb = (u - r * chunks) * 8;
+    const int n = r / H;
+    const int y = r - n * H;
+    const float sy = src_coord(y, Hc, H, sy_scale, ac);
+    const int y0 = static_cast<int>(sy), y1 = min(y0 + 1, Hc - 1);
+    const float wy = sy - static_cast<float>(y0);
+    const int cx0 = static_cast<int>(src_coord(xb, Wc, W, sx_scale, ac));
+    const T* cb = coarse + static_cast<size_t>(n) * Hc * Wc * 256 + lane * 8;
+    const T* crow[2] = {cb + static_cast<size_t>(y0) * Wc * 256,
+                        cb + static_cast<size_t>(y1) * Wc * 256};
+#pragma unroll
+    for (int j = 0; j < kWinCols; ++j) {
+      const int col = min(cx0 + j, Wc - 1);
+      cp_async16(&win[warp][j][lane], crow[0] + static_cast<size_t>(col) * 256);
+      cp_async16(&win[warp][kWinCols + j][lane], crow[1] + static_cast<size_t>(col) * 256);
+    }
+    const size_t io0 = (static_cast<size_t>(r) * W + xb) * 256 + lane * 8;
+    uint4 l[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      l[k] = (lat && xb + k < W) ? *reinterpret_cast<const uint4*>(lat + io0 + k * 256)
+                                 : make_uint4(0u, 0u, 0u, 0u);
+    cp_async_wait_all();
+    if (amax && n != m_img) {  // warp-uniform
+      if (m_img >= 0) publish_amax(amax + m_img, m);
+      m = 0;
+      m_img = n;
+    }
+    auto tap = [&](int row, int xc) -> uint4 {
+      const int j = xc - cx0;
+      return (j >= 0 && j < kWinCols)
+                 ? win[warp][row * kWinCols + j][lane]
+                 : __ldg(reinterpret_cast<const uint4*>(crow[row] + static_cast<size_t>(xc) * 256));
+    };
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int x = xb + k;
+      if (x >= W) break;  // warp-uniform
+      const float sx = src_coord(x, Wc, W, sx_scale, ac);
+      const int x0 = static_cast<int>(sx);
+      const int x1 = min(x0 + 1, Wc - 1);
+      const float wx = sx - static_cast<float>(x0);
+      const float w00 = (1.f - wy) * (1.f - wx), w01 = (1.f - wy) * wx;
+      const float w10 = wy * (1.f - wx), w11 = wy * wx;
+      const uint4 a = tap(0, x0), b = tap(0, x1), c = tap(1, x0), d = tap(1, x1);
+      const uint32_t lw[4] = {l[k].x, l[k].y, l[k].z, l[k].w};
+      const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+      const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+      const uint32_t cw[4] = {c.x, c.y, c.z, c.w};
+      const uint32_t dw[4] = {d.x, d.y, d.z, d.w};
+      uint32_t ow[4], mag = 0;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 fl = lat ? Pair16<T>::unpack(lw[e]) : make_float2(0.f, 0.f);
+        const float2 fa = Pair16<T>::unpack(aw[e]), fb = Pair16<T>::unpack(bw[e]);
+        const float2 fc = Pair16<T>::unpack(cw[e]), fd = Pair16<T>::unpack(dw[e]);
+        float v0 = fmaf(fa.x, w00, fl.x), v1 = fmaf(fa.y, w00, fl.y);
+        v0 = fmaf(fb.x, w01, v0);
+        v1 = fmaf(fb.y, w01, v1);
+        v0 = fmaf(fc.x, w10, v0);
+        v1 = fmaf(fc.y, w10, v1);
+        v0 = fmaf(fd.x, w11, v0);
+        v1 = fmaf(fd.y, w11, v1);
+        ow[e] = Pair16<T>::pack(v0, v1);
+        mag = __vmaxu2(mag, ow[e] & 0x7FFF7FFFu);
+      }
+      if (amax) m = max(m, Pair16<T>::mag_to_f32_bits(mag));
+      *reinterpret_cast<uint4*>(out + io0 + k * 256) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+      if (out_s) {
+        uint32_t sw[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = Pair16<T>::unpack(ow[e]);
+          sw[e] = Pair16<T>::pack(f.x * inv[2 * e], f.y * inv[2 * e + 1]);
+        }
+        *reinterpret_cast<uint4*>(out_s + io0 + k * 256) = make_uint4(sw[0], sw[1], sw[2], sw[3]);
+      }
+    }
+  }
+  if (amax && m_img >= 0) publish_amax(amax + m_img, m);
+}
+
 // ---------------------------------------------------------------- two-level merge
 // M4 = L4 + up(M5) and M3 = L3 + up(M4) in ONE launch (NHWC, 256 channels of a 16-bit type,
 // maps that upsample).  A block owns a kMergeTileH x kMergeTileW tile of M3 and
@@ -1020,6 +1143,28 @@ cudaError_t upsample_add_t(const void* coarse, const void* lat, void* out, int N
         // Maps whose lateral fills half of the L2 or more: interleaved chunks (coarse rows
         // stay in L2; 4 units per thread in flight instead of 2 measured 5 % slower there).
         const bool inter = static_cast<long long>(N) * H * W * 512 > l2_bytes() / 2;
+        // units_per_block 0: one warp per 8-pixel unit where the map upsamples along x
+        // (its taps then fit the unit's coarse window); -1 or > 0: one warp per pixel
+        if (units_per_block == 0 && 7LL * Wc <= 4LL * W && units < (1LL << 31)) {
+          auto ukern = upsample_add_unit_kernel<T>;
+          static std::atomic<int> ures[64];
+          int dev = 0;
+          cudaGetDevice(&dev);
+          const bool cached = dev >= 0 && dev < 64;
+          int res = cached ? ures[dev].load(std::memory_order_relaxed) : 0;
+          if (res == 0) {
+            int per_sm = 0;
+            cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, ukern, 256, 0);
+            if (e != cudaSuccess) return e;
+            res = (per_sm > 0 ? per_sm : 1) * sm_count();
+            if (cached) ures[dev].store(res, std::memory_order_relaxed);
+          }
+          const long long want = (units + 7) / 8;
+          const int grid = static_cast<int>(want < res ? want : res);
+          return launch_ex(ukern, dim3(grid), dim3(256), 0, s, opts, 1, c, l, o, N, Hc, Wc, H, W,
+                           chunks, sy, sx, ac, amax, sc ? static_cast<T*>(sc->out) : nullptr,
+                           sc ? sc->scale_a : nullptr, sc ? sc->scale_w : nullptr);
+        }
         auto kern = upsample_add_px512_kernel<T, kPx512Batch>;
         // grid = the blocks resident at once, each with a contiguous run of units (or, when
         // interleaved, a chunk at a time)
@@ -1037,7 +1182,8 @@ cudaError_t upsample_add_t(const void* coarse, const void* lat, void* out, int N
         }
         const long long g = units < res ? units : res;
         if (g <= 0) return cudaSuccess;
-        const long long per = units_per_block > 0 ? units_per_block : (units + g - 1) / g;
+        const long long per =
+            units_per_block > 0 ? units_per_block : (units + g - 1) / g;  // (-1: automatic)
         if (per >= (1LL << 31)) return cudaErrorInvalidValue;
         const int grid = static_cast<int>((units + per - 1) / per);
         return launch_ex(kern, dim3(grid), dim3(256), 0, s, opts, 1, c, l, o, N, Hc, Wc, H, W,
@@ -1133,7 +1279,7 @@ cudaError_t launch_upsample_add(DType dt, const void* coarse, const void* lat, v
                                 int units_per_block) {
   if (scaled && (!scaled->out || !scaled->scale_a || !scaled->scale_w || !aligned16(scaled->out)))
     return cudaErrorInvalidValue;
-  if (units_per_block < 0) return cudaErrorInvalidValue;
+  if (units_per_block < -1) return cudaErrorInvalidValue;
   switch (dt) {
     case DType::F32:
       if (scaled) return cudaErrorNotSupported;

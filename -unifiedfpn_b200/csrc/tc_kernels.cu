@@ -286,6 +286,7 @@ cudaError_t plan_tc_lateral(TcPlan& plan, DType dt, const void* x, const void* w
   a.out_mode = sc.out_mode;
   a.qamax = sc.qamax;
   a.qscale_out = sc.qscale_out;
+  if (sc.direct_store && !fp8 && sc.out_mode == 0) a.out_direct = out;
   cudaError_t e = encode_nhwc(&plan.map_a, dt, x, N, H, W, Cin, tiling.tile_w, tiling.tile_h);
   if (e != cudaSuccess) return e;
   if ((e = encode_weights(&plan.map_b, dt, w, Cin)) != cudaSuccess) return e;
@@ -499,6 +500,7 @@ cudaError_t tc_set_output_view(TcPlan& plan, void* out, int C, int pix_stride) {
                                   pix_stride, sw, 32 / sw);
   if (e != cudaSuccess) return e;
   a.out_cols = C;
+  a.out_direct = nullptr;  // (the per-warp stores assume a dense 256-channel output)
   std::memcpy(plan.args, &a, sizeof(a));
   return cudaSuccess;
 }
@@ -525,6 +527,7 @@ cudaError_t tc_set_channel_slices(TcPlan& plan, const void* w, int K, int slices
                            32 / sw)) != cudaSuccess)
     return e;
   a.out_cols = C;
+  a.out_direct = nullptr;  // (the per-warp stores assume a dense 256-channel output)
   a.slices = slices;
   a.num_tiles = static_cast<int>(tiles);
   std::memcpy(plan.args, &a, sizeof(a));

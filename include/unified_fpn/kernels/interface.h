@@ -53,8 +53,11 @@ struct MergeScaledCopy {
 };
 // amax_out (optional): amax_out[n] = atomicMax of |out| of image n as fp32 bits (the caller
 // zeroes them first).  scaled (optional): also write the scaled copy.
-// units_per_block (NHWC, 256 channels of a 16-bit type): 8-pixel row units each block walks
-// (0: automatic -- one wave of the blocks resident at once, each with a contiguous run).
+// units_per_block (NHWC, 256 channels of a 16-bit type): 0 = automatic -- one warp per
+// 8-pixel row unit (its lateral vectors and its coarse window loaded at once) where the map
+// upsamples along x (Wc / W <= 4 / 7), else one warp per pixel with one wave of resident
+// blocks, each walking a contiguous run of units; -1 = one warp per pixel, automatic runs;
+// > 0 = one warp per pixel, that many units per block.  The same bits either way.
 cudaError_t launch_upsample_add(DType dt, const void* coarse, const void* lat, void* out, int N,
                                 int C, int Hc, int Wc, int H, int W, int align_corners,
                                 Layout layout, cudaStream_t s, unsigned* amax_out = nullptr,
@@ -188,6 +191,11 @@ struct TcScales {
   // 2 LeakyReLU with act_alpha, 3 Swish); P6 is taken from the activated output.
   int act = 0;
   float act_alpha = 0.01f;
+  // 16-bit lateral (single CTA, out_mode 0) only: each epilogue warp copies its staged rows
+  // to the output with coalesced 16-byte stores (4 pixels x 128 bytes per instruction)
+  // instead of a TMA tensor store, so the output does not queue behind the operand loads in
+  // the SM's TMA unit.  The same bits.
+  bool direct_store = false;
 };
 
 // Lateral 1x1 (+ optional fused bilinear upsample-add of the coarser merged map).

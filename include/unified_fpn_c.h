@@ -146,8 +146,10 @@ int ufpn_core_set_schedule_options(ufpn_core* core, int programmatic_launch, int
  *                            (the same bits)
  *   "p2_parts"          0..8  the P2 level (lateral + 3x3) pipelined over this many groups of
  *                            images (0 / 1: one launch each for the whole batch)
- *   "merge_units"       0..256  8-pixel units per block of the top-down merge kernels (0:
- *                            automatic, one wave of resident blocks)
+ *   "merge_units"     -1..256  form of the top-down merge kernels: 0 = automatic (one warp
+ *                            per 8-pixel unit where the map upsamples along x, else one warp
+ *                            per pixel), -1 = one warp per pixel with automatic runs, > 0 =
+ *                            one warp per pixel with that many 8-pixel units per block
  *   "fp8_two_pass_p2"   0/1  as ufpn_core_set_fp8_options
  *   "grouped_topdown"   0/1  the grouped P5/P4/P3 lateral launch also does the top-down adds
  *                            of M4 and M3 (device-side level counters) instead of two merge

@@ -397,10 +397,13 @@ RAGGED = [(52, 70), (26, 35), (13, 18), (7, 9)]
     {"conv3x3_dynamic": 1}, {"conv3x3_transpose": 0},
     {"conv3x3_p3": -1, "conv3x3_p4": -1, "conv3x3_p5": -1},
     {"conv3x3_p3": -1, "conv3x3_p4": -1, "conv3x3_p5": -1, "conv3x3_dynamic": 1},
+    {"lateral_direct_store": 1}, {"lateral_direct_store": 1, "lateral_wide_epilogue": 1},
+    {"lateral_direct_store": 1, "lateral_tile_p2": 8}, {"merge_units": -1},
 ], ids=["split", "fused", "grouped_topdown", "ksplit", "topdown_ksplit", "merge_two_levels",
         "nsplit", "topdown_nsplit", "nsplit_ksplit", "p2_dynamic", "p2_dynamic_37ctas",
         "lateral_pairs", "lateral_pairs_two_level", "nsplit_single_cta", "conv_claims",
-        "conv_plain_view", "conv_pairs_all_levels", "conv_pairs_all_levels_claims"])
+        "conv_plain_view", "conv_pairs_all_levels", "conv_pairs_all_levels_claims",
+        "lateral_direct", "lateral_direct_wide", "lateral_direct_w8", "merge_warp_per_pixel"])
 def test_neck_ragged_tile_seams(cuda_device, opts):
     """Every schedule option on ragged maps against the oracle (max-norm and per-element),
     bitwise deterministic, and each image alone equals its slice of the batch."""
@@ -484,7 +487,8 @@ def test_grouped_lateral_variants_equal_whole_tiles_bitwise(cuda_device, variant
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_conv3x3_tail_halves_bitwise_at_full_size(cuda_device, dtype):
-    """At the R50 800x1216 batch-2 workload the 3x3s tile the P2 / P3 / P4 maps on their
+    """At the R50 800x1216 batch-2 workload the merges run one warp per 8-pixel unit (the
+    default; merge_units = -1: one warp per pixel) and the 3x3s tile the P2 / P3 / P4 maps on their
     transposed views (conv3x3_transpose, the default: 950 / 260 / 70 tiles instead of 988 /
     266 / 80), and the P2 3x3 on CTA pairs then ends with 31 of 475 pair units on 74 pairs,
     run as channel halves (conv3x3_tail_halves, the default).  The neck is bitwise what plain
@@ -497,7 +501,8 @@ def test_conv3x3_tail_halves_bitwise_at_full_size(cuda_device, dtype):
     xin = [_cl(f.to(dtype).cuda()) for f in host]
     res = []
     for opts in ({}, {"conv3x3_tail_halves": 0}, {"conv3x3_transpose": 0},
-                 {"conv3x3_tail_halves": 0, "conv3x3_transpose": 0}, {"conv3x3_dynamic": 1}):
+                 {"conv3x3_tail_halves": 0, "conv3x3_transpose": 0}, {"conv3x3_dynamic": 1},
+                 {"lateral_direct_store": 1}, {"merge_units": -1}):
         fpn = U.UnifiedFPN()
         for k, v in opts.items():
             fpn.set_option(k, v)
