@@ -681,9 +681,12 @@ int conv3x3_backward(int dtype, const void* x, const void* w, const void* w_f,
       wf = base;
     }
     ufpn::TcPlan plan;
-    // halo tiles on CTA pairs, as the forward engine runs its 3x3s
-    e = ufpn::plan_tc_conv3x3(plan, dt, grad_out, wf, zero_bias, grad_x, nullptr, N, H, W,
-                              ufpn::halo_pair_tiling(), device_status_word(), 0);
+    // halo tiles on CTA pairs, as the forward engine runs its 3x3s (on the map's transposed
+    // view where that needs fewer tiles; the same bits)
+    ufpn::Conv3x3Tiling t = ufpn::halo_pair_tiling();
+    t.transposed = ufpn::halo_transpose_pays(H, W);
+    e = ufpn::plan_tc_conv3x3(plan, dt, grad_out, wf, zero_bias, grad_x, nullptr, N, H, W, t,
+                              device_status_word(), 0);
     if (e == cudaSuccess) e = ufpn::launch_tc(plan, s);
     if (e != cudaSuccess) return cuda_fail(e, "3x3 input gradient");
   }

@@ -68,7 +68,7 @@ __device__ __forceinline__ void pair_settle_ns(uint64_t ns) {
   }
 }
 
-template <typename T, bool kCvt = false>
+template <typename T, bool kCvt = false, bool kClaims = false>
 __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
     fpn_conv3x3_halo_pair_kernel(const __grid_constant__ CUtensorMap map_a,
                                  const __grid_constant__ CUtensorMap map_b,
@@ -114,7 +114,7 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
   // Dynamic claims: every role but the claimer reads the items from the ring; per CTA the
   // readers are the epilogue warps, the converter warps and one thread (the MMA issuer in
   // the leader, the producer in the peer).
-  const bool dyn = args.claim != nullptr;
+  constexpr bool dyn = kClaims;  // (the launcher: kClaims == (args.claim != nullptr))
   constexpr int kClaimReaders = 2 * (kTcEpiWarps + 1 + (kCvt ? kPairCvtWarps : 0));
   ClaimRing ring{claim_rec, cfull_bar, mapa_shared(smem_u32(cempty_bar), 0), 0, 0u};
 
@@ -331,7 +331,7 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
     tc_epilogue<1, T, true>(args, &map_out, tmem_base, accf_bar, acce_bar, smem_stage,
                             abort_flag, warp, lane, false,
                             mapa_shared(smem_u32(acce_bar), 0), nullptr,
-                            dyn ? &ring : nullptr);
+                            kClaims ? &ring : nullptr);
   } else if constexpr (kCvt) {
     // ------------------------------------------------------------ converter (each CTA)
     const int ct = threadIdx.x - 32 * (2 + kTcEpiWarps);  // 0 .. 32 * kPairCvtWarps - 1

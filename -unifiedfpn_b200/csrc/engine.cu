@@ -755,11 +755,9 @@ struct UnifiedFPNCore::Impl {
                   : cudaErrorNotSupported;
       if (pe != cudaSuccess) {
         if (pe != cudaErrorNotSupported) check(pe, "plan lateral pair");
-        ufpn::TcScales lsc;
-        lsc.direct_store = cfg.lateral_direct_store;
         check(ufpn::plan_tc_lateral(lat2, dtype, xin, lat_wp[0], lat_b[0], m3, m2, nb, cin[0],
                                     H[0], W[0], H[1], W[1], lv[0].lat_tiling, d_status,
-                                    p2_lateral_ctas, lsc),
+                                    p2_lateral_ctas),
               "plan lateral");
         ufpn::tc_attach_wb_table(lat2, wb_table);
         if (cfg.lateral_wide_epilogue) ufpn::tc_use_wide_epilogue(lat2);
@@ -1482,7 +1480,6 @@ const std::vector<EngineOption>& engine_options() {
     o.push_back(bool_option<&FPNKernelConfig::conv3x3_tail_halves>("conv3x3_tail_halves"));
     o.push_back(bool_option<&FPNKernelConfig::conv3x3_transpose>("conv3x3_transpose"));
     o.push_back(bool_option<&FPNKernelConfig::conv3x3_dynamic>("conv3x3_dynamic"));
-    o.push_back(bool_option<&FPNKernelConfig::lateral_direct_store>("lateral_direct_store"));
     o.push_back(bool_option<&FPNKernelConfig::grouped_laterals_pair>("grouped_laterals_pair"));
     o.push_back(bool_option<&FPNKernelConfig::fp8_quantise_in_conv>("fp8_quantise_in_conv"));
     o.push_back({"p2_parts", [](int v) { return v >= 0 && v <= 8; },
@@ -1634,7 +1631,6 @@ std::string UnifiedFPNCore::autotune(const void* const* in, void* const* out, vo
     knobs.push_back({"nsplit_p3", {1, 2}});
     knobs.push_back({"programmatic_launch", {1, 0}});
     knobs.push_back({"lateral_wide_epilogue", {0, 1}});
-    knobs.push_back({"lateral_direct_store", {0, 1}});
     {
       const int sms = ufpn::sm_count();
       knobs.push_back({"p2_lateral_ctas", {0, sms * 112 / 148, sms * 128 / 148}});

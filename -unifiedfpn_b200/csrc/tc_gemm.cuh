@@ -182,9 +182,6 @@ struct TcGemmArgs {
   // streams' CTAs still hold it) then take fewer items instead of ending the launch late.
   // null: static round robin over the pairs.
   int* claim;
-  // 16-bit lateral: the output NHWC [N][H][W][256] that the epilogue writes with per-warp
-  // coalesced stores from its staging rows (null: TMA tensor stores through map_out)
-  void* out_direct;
 };
 
 // Work items of a CTA pair claimed at run time: the leader's producer claims each item from
@@ -713,27 +710,7 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
           }
         }
       }
-      if (kMode == 0 && !kPair && omode == 0 && args.out_direct != nullptr) {
-        // The warp's 32 staged rows (pixels) x 128 bytes, 4 pixels per instruction: lane l
-        // takes 16-byte chunk l & 7 of pixel 4 i + (l >> 3) (the chunk sits at (l & 7) ^ (p & 7)
-        // in the swizzled row).  No TMA, no wait for a store to read the staging buffer.
-        __syncwarp();
-        const int c = lane & 7;
-        const int tws = __ffs(tw) - 1;  // tile widths are powers of two
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int p = 4 * i + (lane >> 3);
-          const uint4 v = ld_shared_v4(stage_addr + p * 128 + ((c ^ (p & 7)) << 4));
-          const int r = wrow0 + p;
-          const int gy = y0 + (r >> tws), gx = x0 + (r & (tw - 1));
-          if (real && gy < args.H && gx < args.W) {
-            const size_t pix = (static_cast<size_t>(n) * args.H + gy) * args.W + gx;
-            *reinterpret_cast<uint4*>(static_cast<O*>(args.out_direct) + pix * kTcBlockN +
-                                      col0 + c * 8) = v;
-          }
-        }
-        __syncwarp();  // every lane has read the staging rows before they are rewritten
-      } else if (omode == 0 || (omode == 2 && step == kSteps - 1)) {
+      if (omode == 0 || (omode == 2 && step == kSteps - 1)) {
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {

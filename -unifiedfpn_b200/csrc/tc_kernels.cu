@@ -174,19 +174,28 @@ cudaError_t launch_halo_t(const TcPlan& p, cudaStream_t s, LaunchOpts opts) {
                    HaloCfg::kSmemBytes, s, opts, 1, p.map_a, p.map_b, p.map_out, a);
 }
 
-template <typename T, bool kCvt = false>
-cudaError_t launch_halo_pair_t(const TcPlan& p, cudaStream_t s, LaunchOpts opts) {
+template <typename T, bool kCvt, bool kClaims>
+cudaError_t launch_halo_pair_form(const TcPlan& p, const TcGemmArgs& a, cudaStream_t s,
+                                  LaunchOpts opts) {
+  auto kern = fpn_conv3x3_halo_pair_kernel<T, kCvt, kClaims>;
   static std::atomic<bool> configured[64];
-  cudaError_t e = once_per_device(configured, [] {
-    return cudaFuncSetAttribute(fpn_conv3x3_halo_pair_kernel<T, kCvt>, cudaFuncAttributeMaxDynamicSharedMemorySize, PairCfgT<kCvt>::kSmemBytes);
+  cudaError_t e = once_per_device(configured, [&] {
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                PairCfgT<kCvt>::kSmemBytes);
   });
   if (e != cudaSuccess) return e;
+  // (map_coarse of a CTA-pair 3x3 plan: the 64-row weight box of its channel-half items)
+  return launch_ex(kern, dim3(p.grid), dim3(PairCfgT<kCvt>::kThreads),
+                   PairCfgT<kCvt>::kSmemBytes, s, opts, 2, p.map_a, p.map_b, p.map_out,
+                   p.map_coarse, a);
+}
+template <typename T, bool kCvt = false>
+cudaError_t launch_halo_pair_t(const TcPlan& p, cudaStream_t s, LaunchOpts opts) {
   TcGemmArgs a;
   std::memcpy(&a, p.args, sizeof(a));
-  // (map_coarse of a CTA-pair 3x3 plan: the 64-row weight box of its channel-half items)
-  return launch_ex(fpn_conv3x3_halo_pair_kernel<T, kCvt>, dim3(p.grid),
-                   dim3(PairCfgT<kCvt>::kThreads), PairCfgT<kCvt>::kSmemBytes, s, opts, 2,
-                   p.map_a, p.map_b, p.map_out, p.map_coarse, a);
+  // run-time item claims: a separate instantiation, so the static form carries none of it
+  return a.claim != nullptr ? launch_halo_pair_form<T, kCvt, true>(p, a, s, opts)
+                            : launch_halo_pair_form<T, kCvt, false>(p, a, s, opts);
 }
 
 template <typename T>
@@ -286,7 +295,6 @@ cudaError_t plan_tc_lateral(TcPlan& plan, DType dt, const void* x, const void* w
   a.out_mode = sc.out_mode;
   a.qamax = sc.qamax;
   a.qscale_out = sc.qscale_out;
-  if (sc.direct_store && !fp8 && sc.out_mode == 0) a.out_direct = out;
   cudaError_t e = encode_nhwc(&plan.map_a, dt, x, N, H, W, Cin, tiling.tile_w, tiling.tile_h);
   if (e != cudaSuccess) return e;
   if ((e = encode_weights(&plan.map_b, dt, w, Cin)) != cudaSuccess) return e;
@@ -500,7 +508,6 @@ cudaError_t tc_set_output_view(TcPlan& plan, void* out, int C, int pix_stride) {
                                   pix_stride, sw, 32 / sw);
   if (e != cudaSuccess) return e;
   a.out_cols = C;
-  a.out_direct = nullptr;  // (the per-warp stores assume a dense 256-channel output)
   std::memcpy(plan.args, &a, sizeof(a));
   return cudaSuccess;
 }
@@ -527,7 +534,6 @@ cudaError_t tc_set_channel_slices(TcPlan& plan, const void* w, int K, int slices
                            32 / sw)) != cudaSuccess)
     return e;
   a.out_cols = C;
-  a.out_direct = nullptr;  // (the per-warp stores assume a dense 256-channel output)
   a.slices = slices;
   a.num_tiles = static_cast<int>(tiles);
   std::memcpy(plan.args, &a, sizeof(a));

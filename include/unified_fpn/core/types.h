@@ -192,10 +192,6 @@ struct FPNKernelConfig {
   // Measured slower at R50 800x1216 x 2 (equal-sized items claimed greedily end less evenly
   // than the static deal's 6.5 rounds): off.
   bool conv3x3_dynamic = false;
-  // 16-bit P2 lateral: the epilogue warps write their staged output rows with coalesced
-  // 16-byte stores instead of TMA tensor stores (which queue behind the operand loads in the
-  // SM's TMA unit).  The same bits.
-  bool lateral_direct_store = false;
   // 16-bit split schedule: the grouped raw P5 / P4 / P3 laterals on CTA pairs (each SM
   // streams half of every weight k-block; host-dealt static schedule).  Same bits as the
   // single-CTA grouped launch (false), which split-K, channel halves and top-down adds in

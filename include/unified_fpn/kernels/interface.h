@@ -191,11 +191,6 @@ struct TcScales {
   // 2 LeakyReLU with act_alpha, 3 Swish); P6 is taken from the activated output.
   int act = 0;
   float act_alpha = 0.01f;
-  // 16-bit lateral (single CTA, out_mode 0) only: each epilogue warp copies its staged rows
-  // to the output with coalesced 16-byte stores (4 pixels x 128 bytes per instruction)
-  // instead of a TMA tensor store, so the output does not queue behind the operand loads in
-  // the SM's TMA unit.  The same bits.
-  bool direct_store = false;
 };
 
 // Lateral 1x1 (+ optional fused bilinear upsample-add of the coarser merged map).

@@ -397,13 +397,12 @@ RAGGED = [(52, 70), (26, 35), (13, 18), (7, 9)]
     {"conv3x3_dynamic": 1}, {"conv3x3_transpose": 0},
     {"conv3x3_p3": -1, "conv3x3_p4": -1, "conv3x3_p5": -1},
     {"conv3x3_p3": -1, "conv3x3_p4": -1, "conv3x3_p5": -1, "conv3x3_dynamic": 1},
-    {"lateral_direct_store": 1}, {"lateral_direct_store": 1, "lateral_wide_epilogue": 1},
-    {"lateral_direct_store": 1, "lateral_tile_p2": 8}, {"merge_units": -1},
+    {"merge_units": -1},
 ], ids=["split", "fused", "grouped_topdown", "ksplit", "topdown_ksplit", "merge_two_levels",
         "nsplit", "topdown_nsplit", "nsplit_ksplit", "p2_dynamic", "p2_dynamic_37ctas",
         "lateral_pairs", "lateral_pairs_two_level", "nsplit_single_cta", "conv_claims",
         "conv_plain_view", "conv_pairs_all_levels", "conv_pairs_all_levels_claims",
-        "lateral_direct", "lateral_direct_wide", "lateral_direct_w8", "merge_warp_per_pixel"])
+        "merge_warp_per_pixel"])
 def test_neck_ragged_tile_seams(cuda_device, opts):
     """Every schedule option on ragged maps against the oracle (max-norm and per-element),
     bitwise deterministic, and each image alone equals its slice of the batch."""
@@ -502,7 +501,7 @@ def test_conv3x3_tail_halves_bitwise_at_full_size(cuda_device, dtype):
     res = []
     for opts in ({}, {"conv3x3_tail_halves": 0}, {"conv3x3_transpose": 0},
                  {"conv3x3_tail_halves": 0, "conv3x3_transpose": 0}, {"conv3x3_dynamic": 1},
-                 {"lateral_direct_store": 1}, {"merge_units": -1}):
+                 {"merge_units": -1}):
         fpn = U.UnifiedFPN()
         for k, v in opts.items():
             fpn.set_option(k, v)
