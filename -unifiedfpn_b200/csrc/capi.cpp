@@ -487,15 +487,17 @@ int ufpn_conv3x3_act(int dtype, const void* x, const void* w, const float* bias,
     t.tile_w = tile_w;
     t.tile_h = 128 / tile_w;
     t.halo = false;
-  } else if (tile_w == -1 || tile_w == -3) {
+  } else if (tile_w == -1 || tile_w == -3 || tile_w == -5) {
     t = ufpn::halo_pair_tiling();
-  } else if (tile_w < -3) {
+  } else if (tile_w < -5) {
     return fail(UFPN_ERR_INVALID_ARG,
                 "tile_w must be 0 (halo tiling), -1 (halo tiling on CTA pairs), -2 / -3 (the "
-                "same on the map's transposed view) or 8..128");
+                "same on the map's transposed view), -4 / -5 (mixed) or 8..128");
   }
   t.transposed = tile_w == -2 || tile_w == -3;
-  if (t.transposed && p6) return fail(UFPN_ERR_INVALID_ARG, "transposed view: no fused P6");
+  t.mixed = tile_w == -4 || tile_w == -5;
+  if ((t.transposed || t.mixed) && p6)
+    return fail(UFPN_ERR_INVALID_ARG, "transposed or mixed view: no fused P6");
   int* status = device_status_word();
   ufpn::TcPlan plan;
   ufpn::TcScales sc;
@@ -684,7 +686,10 @@ int conv3x3_backward(int dtype, const void* x, const void* w, const void* w_f,
     // halo tiles on CTA pairs, as the forward engine runs its 3x3s (on the map's transposed
     // view where that needs fewer tiles; the same bits)
     ufpn::Conv3x3Tiling t = ufpn::halo_pair_tiling();
-    t.transposed = ufpn::halo_transpose_pays(H, W);
+    if (ufpn::halo_mixed_pays(N, H, W, true))
+      t.mixed = true;
+    else
+      t.transposed = ufpn::halo_transpose_pays(H, W);
     e = ufpn::plan_tc_conv3x3(plan, dt, grad_out, wf, zero_bias, grad_x, nullptr, N, H, W, t,
                               device_status_word(), 0);
     if (e == cudaSuccess) e = ufpn::launch_tc(plan, s);
@@ -1014,14 +1019,16 @@ int ufpn_conv3x3_e4m3(const void* x, const float* x_scale, int x_scale_per_image
   sc.ascale_per_image = x_scale_per_image != 0;
   sc.wscale = w_scales;
   sc.amax_out = amax_out;
-  if (tile_w > 0 || tile_w < -3)
+  if (tile_w > 0 || tile_w < -5)
     return fail(UFPN_ERR_INVALID_ARG,
-                "e4m3 3x3: tile_w must be 0 (halo), -1 (halo, CTA pairs) or -2 / -3 (the same "
-                "on the map's transposed view)");
-  ufpn::Conv3x3Tiling t =
-      tile_w == -1 || tile_w == -3 ? ufpn::halo_pair_tiling() : ufpn::halo_tiling();
+                "e4m3 3x3: tile_w must be 0 (halo), -1 (halo, CTA pairs), -2 / -3 (the same "
+                "on the map's transposed view) or -4 / -5 (mixed)");
+  ufpn::Conv3x3Tiling t = tile_w == -1 || tile_w == -3 || tile_w == -5 ? ufpn::halo_pair_tiling()
+                                                                      : ufpn::halo_tiling();
   t.transposed = tile_w == -2 || tile_w == -3;
-  if (t.transposed && p6) return fail(UFPN_ERR_INVALID_ARG, "transposed view: no fused P6");
+  t.mixed = tile_w == -4 || tile_w == -5;
+  if ((t.transposed || t.mixed) && p6)
+    return fail(UFPN_ERR_INVALID_ARG, "transposed or mixed view: no fused P6");
   ufpn::TcPlan plan;
   cudaError_t e = ufpn::plan_tc_conv3x3(plan, DType::E4M3, x, w, bias, out, p6, N, H, W, t,
                                         device_status_word(), 0, sc);

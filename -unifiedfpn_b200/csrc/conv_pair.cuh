@@ -74,6 +74,8 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
                                  const __grid_constant__ CUtensorMap map_b,
                                  const __grid_constant__ CUtensorMap map_out,
                                  const __grid_constant__ CUtensorMap map_bh,
+                                 const __grid_constant__ CUtensorMap map_a2,
+                                 const __grid_constant__ CUtensorMap map_out2,
                                  const TcGemmArgs args) {
   static_assert(!kCvt || TcElem<T>::kFp8, "the converter quantises to e4m3");
   using Cfg = PairCfgT<kCvt>;
@@ -144,6 +146,10 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
     prefetch_tmap(&map_b);
     prefetch_tmap(&map_out);
     if (args.pair_tail > 0) prefetch_tmap(&map_bh);
+    if (args.strip_first > 0) {
+      prefetch_tmap(&map_a2);
+      prefetch_tmap(&map_out2);
+    }
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, kTcTmemCols);
@@ -202,8 +208,9 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
                                   : half * (kTcBlockN / 2) + static_cast<int>(rank) * (kTcBlockN / 4);
         const CUtensorMap* mb = half < 0 ? &map_b : &map_bh;
         const uint32_t bbytes = half < 0 ? 2 * kPairBStage : kPairBStage;  // both CTAs
-        int n, x0, y0;
-        tc_tile_origin(args, 2 * u + static_cast<int>(rank), n, x0, y0);
+        const HaloTile ht = halo_tile(args, 2 * u + static_cast<int>(rank));
+        const int n = ht.n, x0 = ht.x0, y0 = ht.y0;
+        const CUtensorMap* ma = ht.strip ? &map_a2 : &map_a;
         for (int cb = 0; ok && cb < cin_blocks; ++cb) {
           if (dyn && leader && cb == cin_blocks - 1 && !claim_begin()) {
             ok = false;
@@ -218,7 +225,7 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
             }
             mbar_arrive_expect_tx(rfull_bar, 2 * kHaloRows * 128);
             for (int j = 0; j < 2; ++j)
-              tma_load_4d(smem_rawbuf + j * kHaloBytes, &map_a, rfull_bar, cb * 128 + j * 64,
+              tma_load_4d(smem_rawbuf + j * kHaloBytes, ma, rfull_bar, cb * 128 + j * 64,
                           x0 - 1, y0 - 1, n, kPolicyEvictLast);
             rphase ^= 1u;
           } else {
@@ -228,7 +235,7 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
               break;
             }
             if (leader) mbar_arrive_expect_tx(&hfull_bar[hb], 2 * kHaloRows * 128);
-            tma_load_4d_pair(smem_halo + hb * kHaloBytes, &map_a, hfull0 + hb * 8u,
+            tma_load_4d_pair(smem_halo + hb * kHaloBytes, ma, hfull0 + hb * 8u,
                              cb * kKbElems<T>, x0 - 1, y0 - 1, n, kPolicyEvictLast);
             if (++hb == kHaloBufs) {
               hb = 0;
@@ -276,8 +283,10 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
         if (dyn && !ring.next(it, abort_flag, args.status, kDevTimeoutMma)) break;
         if (!ok || it >= items) break;
         int half;
-        pair_item_unit(args, units, it, half);
+        const int u = pair_item_unit(args, units, it, half);
         const uint32_t idesc = half < 0 ? idesc_full : idesc_half;
+        // (both tiles of a unit are of one view: one tap offset for both CTAs' halos)
+        const int tr = halo_tile(args, 2 * u).tr;
         if (!mbar_wait(&acce_bar[acc], acc_phase ^ 1u, abort_flag, args.status, kDevTimeoutMma))
           break;
         tc_fence_after();
@@ -296,7 +305,7 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
             }
             tc_fence_after();
             const uint64_t adesc = sdesc_kmajor_sw128_stride(
-                halo_addr + static_cast<uint32_t>(halo_tap_offset(tap, args.transposed) * 128),
+                halo_addr + static_cast<uint32_t>(halo_tap_offset(tap, tr) * 128),
                 (kHaloTileW + 2) * 128);
             const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(smem_b + stage * kPairBStage));
 #pragma unroll
@@ -331,7 +340,7 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
     tc_epilogue<1, T, true>(args, &map_out, tmem_base, accf_bar, acce_bar, smem_stage,
                             abort_flag, warp, lane, false,
                             mapa_shared(smem_u32(acce_bar), 0), nullptr,
-                            kClaims ? &ring : nullptr);
+                            kClaims ? &ring : nullptr, &map_out2);
   } else if constexpr (kCvt) {
     // ------------------------------------------------------------ converter (each CTA)
     const int ct = threadIdx.x - 32 * (2 + kTcEpiWarps);  // 0 .. 32 * kPairCvtWarps - 1
@@ -345,8 +354,7 @@ __global__ void __launch_bounds__(PairCfgT<kCvt>::kThreads, 1)
       if (!ok || it >= items) break;
       int half;
       const int tile = 2 * pair_item_unit(args, units, it, half) + static_cast<int>(rank);
-      int n, x0, y0;
-      tc_tile_origin(args, tile, n, x0, y0);
+      const int n = halo_tile(args, tile).n;
       // virtual tile (past the end): its halo is all padding, any finite scale will do
       const unsigned am = tile < args.num_tiles ? __ldg(args.in_amax + n) : 0u;
       const float inv = e4m3_inv_of(am);

@@ -452,9 +452,16 @@ struct UnifiedFPNCore::Impl {
   int* conv_claim(int l) const { return cfg.conv3x3_dynamic ? d_sched + 32 + 2 * l : nullptr; }
   // The 3x3 tiling of level l launched on its own: halo tiles on the map's transposed view
   // where that needs fewer tiles (conv3x3_transpose), except with the fused P6 output.
-  Conv3x3Tiling conv_tiling_for(int l, Conv3x3Tiling t, bool with_p6) const {
-    t.transposed = t.halo && !with_p6 && cfg.conv3x3_transpose &&
-                   ufpn::halo_transpose_pays(H[l], W[l]);
+  // (conv3x3_mixed: the own view for the whole 16-row tile rows and the transposed view for
+  // the remaining strip, where that needs no more tiles than the transposed view.)
+  Conv3x3Tiling conv_tiling_for(int l, Conv3x3Tiling t, bool with_p6, int images) const {
+    t.transposed = false;
+    t.mixed = false;
+    if (!t.halo || with_p6 || !cfg.conv3x3_transpose) return t;
+    if (cfg.conv3x3_mixed && ufpn::halo_mixed_pays(images, H[l], W[l], t.pair))
+      t.mixed = true;
+    else
+      t.transposed = ufpn::halo_transpose_pays(H[l], W[l]);
     return t;
   }
 
@@ -640,7 +647,7 @@ struct UnifiedFPNCore::Impl {
       void* const p6_out = l == 3 ? o6 : nullptr;
       check(ufpn::plan_tc_conv3x3(conv, dtype, merged[l], out_wp[l], out_b[l], o[l], p6_out,
                                   batch, H[l], W[l],
-                                  conv_tiling_for(l, tiling_for(l), p6_out != nullptr),
+                                  conv_tiling_for(l, tiling_for(l), p6_out != nullptr, batch),
                                   d_status, 0, act_scales(), conv_claim(l)),
             "plan conv3x3");
       // (on the main stream the 3x3 follows a kernel: the P2 lateral, or the previous
@@ -784,7 +791,7 @@ struct UnifiedFPNCore::Impl {
         check(ufpn::plan_tc_conv3x3(conv, dtype, static_cast<char*>(merged[0]) + px0 * cout * esz,
                                     out_wp[0], out_b[0], static_cast<char*>(o[0]) + px0 * cout * esz,
                                     nullptr, n1 - n0, H[0], W[0],
-                                    conv_tiling_for(0, tiling_for(0), false), d_status, 0,
+                                    conv_tiling_for(0, tiling_for(0), false, n1 - n0), d_status, 0,
                                     act_scales()),
               "plan conv3x3");
         ok(ufpn::launch_tc(conv, p2_side), "conv3x3 launch");
@@ -892,7 +899,7 @@ struct UnifiedFPNCore::Impl {
       const long long n = static_cast<long long>(batch) * H[l] * W[l] * cout;
       Conv3x3Tiling t = tiling_for(l);
       if (!t.halo) t = ufpn::halo_pair_tiling();  // e4m3 runs halo tiles only
-      t = conv_tiling_for(l, t, l == 3 && p6 != nullptr);
+      t = conv_tiling_for(l, t, l == 3 && p6 != nullptr, batch);
       // The CTA-pair 3x3 can quantise M_l itself (per image, in shared memory; no quantise
       // pass, no e4m3 copy of M_l; fp8_quantise_in_conv), but its bf16 staging costs two of
       // the eight weight stages of this weight-feed-bound kernel: measured 240 us against
@@ -1479,6 +1486,7 @@ const std::vector<EngineOption>& engine_options() {
     o.push_back(bool_option<&FPNKernelConfig::lateral_wide_epilogue>("lateral_wide_epilogue"));
     o.push_back(bool_option<&FPNKernelConfig::conv3x3_tail_halves>("conv3x3_tail_halves"));
     o.push_back(bool_option<&FPNKernelConfig::conv3x3_transpose>("conv3x3_transpose"));
+    o.push_back(bool_option<&FPNKernelConfig::conv3x3_mixed>("conv3x3_mixed"));
     o.push_back(bool_option<&FPNKernelConfig::conv3x3_dynamic>("conv3x3_dynamic"));
     o.push_back(bool_option<&FPNKernelConfig::grouped_laterals_pair>("grouped_laterals_pair"));
     o.push_back(bool_option<&FPNKernelConfig::fp8_quantise_in_conv>("fp8_quantise_in_conv"));
@@ -1645,6 +1653,7 @@ std::string UnifiedFPNCore::autotune(const void* const* in, void* const* out, vo
     knobs.push_back({"fp8_quantise_in_conv", {0, 1}});
   }
   knobs.push_back({"conv3x3_transpose", {1, 0}});
+  knobs.push_back({"conv3x3_mixed", {1, 0}});
   knobs.push_back({"conv3x3_dynamic", {1, 0}});
   knobs.push_back({"merge_units", {0, -1, 2, 4, 8, 16}});
   knobs.push_back({"merge_two_levels", {0, 1}});

@@ -182,6 +182,13 @@ struct TcGemmArgs {
   // streams' CTAs still hold it) then take fewer items instead of ending the launch late.
   // null: static round robin over the pairs.
   int* claim;
+  // halo 3x3 with a mixed tiling (strip_first > 0): tiles [0, strip_first) on the map's own
+  // view (tiles_x x tiles_y per image, the tile rows covering the first 16 tiles_y rows of
+  // the map), tiles from strip_first on the transposed view, through the second pair of
+  // tensor maps: the strip of rows [strip_y0, H) (at most 8), strip_tx tiles of 16 columns
+  // per image.  strip_first is even for CTA pairs (a pair's two tiles share one tap offset).
+  int strip_first;
+  int strip_y0, strip_tx;
 };
 
 // Work items of a CTA pair claimed at run time: the leader's producer claims each item from
@@ -233,6 +240,46 @@ __device__ __forceinline__ void claim_publish(volatile int* rec, uint64_t* full,
   const uint32_t f = smem_u32(&full[slot]);
   mbar_arrive_cluster(mapa_shared(f, 1));
   mbar_arrive_cluster(mapa_shared(f, 0));
+}
+
+// Halo 3x3 tiles: 8 wide x 16 high in the view the kernel runs on.
+constexpr int kHaloTileW = 8;
+constexpr int kHaloTileH = 16;
+constexpr int kHaloRows = (kHaloTileW + 2) * (kHaloTileH + 2);  // 180
+// Halo row offset of weight tap `tap` (ky * 3 + kx).  On the transposed view of a map (rows
+// and columns swapped) the same tap shifts the halo by (kx, ky).
+__device__ __forceinline__ int halo_tap_offset(int tap, int transposed) {
+  const int ky = tap / 3, kx = tap - 3 * (tap / 3);
+  return transposed ? kx * (kHaloTileW + 2) + ky : ky * (kHaloTileW + 2) + kx;
+}
+// One halo tile: its image, origin in the coordinates of the view it runs on (x0 along the
+// view's rows, y0 down its columns), whether its taps are mirrored (transposed view), and
+// whether it is a strip tile of a mixed tiling (second pair of tensor maps).
+struct HaloTile {
+  int n, x0, y0;
+  int tr;
+  bool strip;
+};
+__device__ __forceinline__ HaloTile halo_tile(const TcGemmArgs& a, int tile) {
+  HaloTile t;
+  if (a.strip_first > 0 && tile >= a.strip_first) {
+    const int s = tile - a.strip_first;
+    t.n = s / a.strip_tx;
+    t.x0 = a.strip_y0;                        // rows [strip_y0, strip_y0 + 8)
+    t.y0 = (s - t.n * a.strip_tx) * kHaloTileH;  // columns [16 i, 16 i + 16)
+    t.tr = 1;
+    t.strip = true;
+    return t;
+  }
+  const int tx = tile % a.tiles_x;
+  const int t2 = tile / a.tiles_x;
+  const int ty = t2 % a.tiles_y;
+  t.n = t2 / a.tiles_y;
+  t.x0 = tx * a.tile_w;
+  t.y0 = ty * a.tile_h;
+  t.tr = a.transposed;
+  t.strip = false;
+  return t;
 }
 
 // Work items of a CTA-pair 3x3: units [0, units - pair_tail) whole (half = -1), then two
@@ -476,7 +523,8 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
                                             volatile int* abort_flag, int warp, int lane,
                                             bool bil_mma, uint32_t leader_acce = 0,
                                             const float* bias_s = nullptr,
-                                            ClaimRing* ring = nullptr) {
+                                            ClaimRing* ring = nullptr,
+                                            const CUtensorMap* map_out2 = nullptr) {
   using O = typename TcElem<T>::Out;
   constexpr bool kFp8 = TcElem<T>::kFp8;
   // kEpiW / 4 warps share each TMEM lane quarter; each owns kChans output channels,
@@ -516,14 +564,29 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
     tc_fence_after();
 
     int n, x0, y0, slice = 0;
-    if constexpr (kMode == 0 && !kPair)
+    // the tile's view: a strip tile of a mixed 3x3 tiling runs on the transposed view (its
+    // rows along the map's columns) and stores through the second output map
+    const CUtensorMap* mo = map_out;
+    int vH = args.H, vW = args.W;
+    if constexpr (kMode == 0 && !kPair) {
       tc_tile_origin(args, tile, n, x0, y0, slice);
-    else
+    } else if constexpr (kMode == 1) {
+      const HaloTile ht = halo_tile(args, tile);
+      n = ht.n;
+      x0 = ht.x0;
+      y0 = ht.y0;
+      if (ht.strip) {
+        mo = map_out2;
+        vH = args.W;
+        vW = args.H;
+      }
+    } else {
       tc_tile_origin(args, tile, n, x0, y0);
+    }
     const int scol = slice * kTcBlockN;  // channel offset of this tile's output slice
     const int py = y0 + row / tw;
     const int px = x0 + row % tw;
-    const bool valid = real && (py < args.H) && (px < args.W);
+    const bool valid = real && (py < vH) && (px < vW);
     const float ascale = !(kFp8 && real) ? 1.f
                          : args.in_amax != nullptr ? e4m3_scale_of(__ldg(args.in_amax + n))
                                                    : __ldg(args.ascale + n * args.ascale_stride);
@@ -717,7 +780,7 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
           // e4m3: the warp's 128 channels (128 bytes per pixel) in one store.  Every buffer
           // use commits a group (empty for virtual tiles) so group counts stay in step.
           if (real && (omode != 0 || args.out_cols == 0 || scol + col0 < args.out_cols))
-            tma_store_4d(map_out, my_stage + sbuf * kTcStagingPerWarp,
+            tma_store_4d(mo, my_stage + sbuf * kTcStagingPerWarp,
                          omode == 0 ? scol + col0 : chalf * kChans, ox, oy, n);
           bulk_commit_group();
         }
@@ -977,15 +1040,6 @@ __global__ void __launch_bounds__(TcCfgT<kMode, T, kWideEpi>::kThreads, 1)
 // atom, successive atoms are a constant 10 rows (1280 bytes) apart -- a plain
 // K-major descriptor with that stride.  Per tile this moves 4 x 23 KB of activations
 // instead of 36 x 16 KB; only the weights stream per tap.
-constexpr int kHaloTileW = 8;
-constexpr int kHaloTileH = 16;
-constexpr int kHaloRows = (kHaloTileW + 2) * (kHaloTileH + 2);  // 180
-// Halo row offset of weight tap `tap` (ky * 3 + kx).  On the transposed view of a map (rows
-// and columns swapped) the same tap shifts the halo by (kx, ky).
-__device__ __forceinline__ int halo_tap_offset(int tap, int transposed) {
-  const int ky = tap / 3, kx = tap - 3 * (tap / 3);
-  return transposed ? kx * (kHaloTileW + 2) + ky : ky * (kHaloTileW + 2) + kx;
-}
 constexpr int kHaloBytes = ((kHaloRows * 128 + 1023) / 1024) * 1024;
 constexpr int kHaloStages = 4;  // weight stages
 constexpr int kHaloBufs = 2;    // halo buffers
@@ -1017,7 +1071,9 @@ template <typename T>
 __global__ void __launch_bounds__(kTcThreads, 1)
     fpn_conv3x3_halo_kernel(const __grid_constant__ CUtensorMap map_a,
                             const __grid_constant__ CUtensorMap map_b,
-                            const __grid_constant__ CUtensorMap map_out, const TcGemmArgs args) {
+                            const __grid_constant__ CUtensorMap map_out,
+                            const __grid_constant__ CUtensorMap map_a2,
+                            const __grid_constant__ CUtensorMap map_out2, const TcGemmArgs args) {
   constexpr int S = kHaloStages;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -1059,6 +1115,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     prefetch_tmap(&map_a);
     prefetch_tmap(&map_b);
     prefetch_tmap(&map_out);
+    if (args.strip_first > 0) {
+      prefetch_tmap(&map_a2);
+      prefetch_tmap(&map_out2);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTcTmemCols);
@@ -1077,8 +1137,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       uint32_t phase = 0, hphase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < args.num_tiles; tile += gridDim.x) {
-        int n, x0, y0;
-        tc_tile_origin(args, tile, n, x0, y0);
+        const HaloTile ht = halo_tile(args, tile);
+        const int n = ht.n, x0 = ht.x0, y0 = ht.y0;
+        const CUtensorMap* ma = ht.strip ? &map_a2 : &map_a;
         for (int cb = 0; ok && cb < cin_blocks; ++cb) {
           if (!mbar_wait(&hempty_bar[hb], hphase ^ 1u, abort_flag, args.status,
                          kDevTimeoutProducer)) {
@@ -1086,7 +1147,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             break;
           }
           mbar_arrive_expect_tx(&hfull_bar[hb], kHaloRows * 128);
-          tma_load_4d(smem_halo + hb * kHaloBytes, &map_a, &hfull_bar[hb], cb * kKbElems<T>, x0 - 1,
+          tma_load_4d(smem_halo + hb * kHaloBytes, ma, &hfull_bar[hb], cb * kKbElems<T>, x0 - 1,
                       y0 - 1, n, kPolicyEvictLast);
           ++hissued;
           if (++hb == kHaloBufs) {
@@ -1139,6 +1200,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kTcBlockN);
+        const int tr = halo_tile(args, tile).tr;
         for (int cb = 0; ok && cb < cin_blocks; ++cb) {
           if (!mbar_wait(&hfull_bar[hb], hphase, abort_flag, args.status, kDevTimeoutMma)) {
             ok = false;
@@ -1153,7 +1215,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             tc_fence_after();
             const uint64_t adesc = sdesc_kmajor_sw128_stride(
-                halo_addr + static_cast<uint32_t>(halo_tap_offset(tap, args.transposed) * 128),
+                halo_addr + static_cast<uint32_t>(halo_tap_offset(tap, tr) * 128),
                 (kHaloTileW + 2) * 128);
             const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(smem_b + stage * kTcBStage));
 #pragma unroll
@@ -1185,7 +1247,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else {
     tc_epilogue<1, T>(args, &map_out, tmem_base, accf_bar, acce_bar, smem_stage, abort_flag, warp,
-                      lane, false);
+                      lane, false, 0, nullptr, nullptr, &map_out2);
   }
 
   tc_fence_before();

@@ -171,7 +171,8 @@ cudaError_t launch_halo_t(const TcPlan& p, cudaStream_t s, LaunchOpts opts) {
   TcGemmArgs a;
   std::memcpy(&a, p.args, sizeof(a));
   return launch_ex(fpn_conv3x3_halo_kernel<T>, dim3(p.grid), dim3(kTcThreads),
-                   HaloCfg::kSmemBytes, s, opts, 1, p.map_a, p.map_b, p.map_out, a);
+                   HaloCfg::kSmemBytes, s, opts, 1, p.map_a, p.map_b, p.map_out, p.map_a2,
+                   p.map_out2, a);
 }
 
 template <typename T, bool kCvt, bool kClaims>
@@ -187,7 +188,7 @@ cudaError_t launch_halo_pair_form(const TcPlan& p, const TcGemmArgs& a, cudaStre
   // (map_coarse of a CTA-pair 3x3 plan: the 64-row weight box of its channel-half items)
   return launch_ex(kern, dim3(p.grid), dim3(PairCfgT<kCvt>::kThreads),
                    PairCfgT<kCvt>::kSmemBytes, s, opts, 2, p.map_a, p.map_b, p.map_out,
-                   p.map_coarse, a);
+                   p.map_coarse, p.map_a2, p.map_out2, a);
 }
 template <typename T, bool kCvt = false>
 cudaError_t launch_halo_pair_t(const TcPlan& p, cudaStream_t s, LaunchOpts opts) {
@@ -374,11 +375,26 @@ cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w
   // map's own).
   const bool tr = tiling.transposed;
   if (tr && (!tiling.halo || p6 != nullptr)) return cudaErrorInvalidValue;
+  // Mixed tiling: the own view for rows [0, 16 floor(H/16)), the transposed view for the
+  // strip of the remaining 1..8 rows.
+  const bool mixed = tiling.mixed;
+  if (mixed && (!tiling.halo || tr || p6 != nullptr || H < 16 || H % 16 == 0 || H % 16 > 8))
+    return cudaErrorInvalidValue;
   TcGemmArgs a;
   std::memset(&a, 0, sizeof(a));
   fill_tiling(a, N, tr ? W : H, tr ? H : W, tiling);
   a.transposed = tr ? 1 : 0;
-  const long long tiles = static_cast<long long>(a.tiles_x) * a.tiles_y * N;
+  long long tiles = static_cast<long long>(a.tiles_x) * a.tiles_y * N;
+  if (mixed) {
+    a.tiles_y = H / kHaloTileH;  // whole 16-row tile rows on the own view
+    const long long own = static_cast<long long>(a.tiles_x) * a.tiles_y * N;
+    if (tiling.pair && own % 2 != 0) return cudaErrorInvalidValue;
+    a.strip_y0 = a.tiles_y * kHaloTileH;
+    a.strip_tx = (W + kHaloTileH - 1) / kHaloTileH;
+    tiles = own + static_cast<long long>(a.strip_tx) * N;
+    if (tiles >= (1LL << 31)) return cudaErrorInvalidValue;
+    a.strip_first = static_cast<int>(own);
+  }
   if (tiles >= (1LL << 31)) return cudaErrorInvalidValue;
   a.num_tiles = static_cast<int>(tiles);
   a.cin_blocks = C / (128 / dtype_size(dt));
@@ -406,12 +422,20 @@ cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w
                                      kHaloTileW + 2, kHaloTileH + 2, 128, tr)
                        : encode_nhwc(&plan.map_a, dt, x, N, H, W, C, tiling.tile_w, tiling.tile_h);
   if (e != cudaSuccess) return e;
+  plan.map_a2 = plan.map_a;  // (unused unless mixed)
+  if (mixed && (e = encode_nhwc(&plan.map_a2, cvt ? DType::BF16 : dt, x, N, H, W, C,
+                                kHaloTileW + 2, kHaloTileH + 2, 128, true)) != cudaSuccess)
+    return e;
   if ((e = encode_weights(&plan.map_b, dt, w, 9 * C, tiling.pair ? kTcBlockN / 2 : kTcBlockN)) !=
       cudaSuccess)
     return e;
   const int sw = tiling.tile_w < 32 ? tiling.tile_w : 32;
   if ((e = encode_nhwc(&plan.map_out, odt, out, N, H, W, kTcBlockN, sw, 32 / sw, 128, tr)) !=
       cudaSuccess)
+    return e;
+  plan.map_out2 = plan.map_out;
+  if (mixed && (e = encode_nhwc(&plan.map_out2, odt, out, N, H, W, kTcBlockN, sw, 32 / sw, 128,
+                                true)) != cudaSuccess)
     return e;
   plan.map_coarse = plan.map_out;
   plan.mode = cvt ? 4 : (tiling.pair ? 3 : (halo ? 2 : 1));

@@ -115,8 +115,9 @@ def fpn_conv3x3(input: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, p
     P6 = max_pool2d(out, 1, 2).  ``weight`` is [256, 256, 3, 3] (any float dtype)
     or, for 16-bit inputs, already packed [256, 9, 256] by :func:`pack_conv3x3_weight`.
     ``tile_w``: 0 = 8x16 halo tiles, -1 = halo tiles on CTA pairs, -2 / -3 = the same on the
-    map's transposed view (16 columns x 8 rows per tile; not with ``p6``), 8..128 = plain
-    tiles.
+    map's transposed view (16 columns x 8 rows per tile; not with ``p6``), -4 / -5 = a mixed
+    tiling (the own view for the whole 16-row tile rows, the transposed view for the last
+    1..8 rows; not with ``p6``), 8..128 = plain tiles.
     ``activation`` ("relu", "leaky_relu" with negative slope ``alpha``, "swish") is applied
     in the epilogue after the bias (P6 comes from the activated output); reference:
     activation_kernel (lib/kernels/compute/fpn_compute_kernels.cu:373-395).

@@ -727,11 +727,16 @@ def main():
             memory_format=torch.channels_last)
         w3 = torch.randn(256, 256, 3, 3, device=dev, generator=gen) * 0.03
         bias = torch.zeros(256, device=dev)
-        # the engine's form: halo tiles on CTA pairs, on the map's transposed view when that
-        # needs fewer 8 x 16 tiles (tile_w -3; 200 x 304: 475 instead of 494 per image)
+        # the engine's form: halo tiles on CTA pairs, with the mixed tiling (tile_w -5: the own
+        # view for whole 16-row tile rows, the transposed view for the last 1..8 rows) or the
+        # transposed view (-3) when that needs fewer 8 x 16 tiles (200 x 304: 475 instead of 494
+        # per image)
         plain_tiles = -(-w2 // 8) * -(-h2 // 16)
         trans_tiles = -(-h2 // 8) * -(-w2 // 16)
-        tw = -3 if trans_tiles < plain_tiles else -1
+        mixed_tiles = -(-w2 // 8) * (h2 // 16) + -(-w2 // 16)
+        mixed_ok = (h2 >= 16 and 0 < h2 % 16 <= 8 and (B * -(-w2 // 8) * (h2 // 16)) % 2 == 0
+                    and mixed_tiles < plain_tiles and mixed_tiles <= trans_tiles)
+        tw = -5 if mixed_ok else (-3 if trans_tiles < plain_tiles else -1)
         if fp8:
             xq, xs = U.quantize_fp8(xr, per_image=True)
             wq, wsc = U.quantize_fp8_rows(w3, pack3x3=True)

@@ -186,6 +186,11 @@ struct FPNKernelConfig {
   // Halo 3x3s on the map's transposed view (tiles of 16 columns x 8 rows) wherever that
   // needs fewer tiles (200 x 304: 475 instead of 494 per image).  The same bits.
   bool conv3x3_transpose = true;
+  // With conv3x3_transpose: where it needs no more tiles than the transposed view, a mixed
+  // tiling -- the map's own view for the rows that fill whole 16-row tiles, the transposed
+  // view only for the remaining strip of at most 8 rows (200 x 304: 456 + 19 tiles per
+  // image).  The same bits.
+  bool conv3x3_mixed = true;
   // 3x3s on CTA pairs claim their work items at run time (a device counter) instead of a
   // static round robin, so that pairs that reach an SM late, while other streams' CTAs hold
   // it, take fewer items.  Each item's results do not depend on which pair runs it.

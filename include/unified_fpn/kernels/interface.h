@@ -125,6 +125,13 @@ struct Conv3x3Tiling {
   // rows.  Each output element accumulates the same k-blocks in the same order: the results
   // are bitwise those of the untransposed conv.  Not with a fused P6 output.
   bool transposed = false;
+  // Halo tiles only (not with transposed, not with a fused P6 output): a mixed tiling -- the
+  // map's own view for the rows that fill whole 16-row tiles and the transposed view for the
+  // remaining strip of at most 8 rows (200 x 304: 12 rows of 38 tiles + 19 strip tiles, 475
+  // per image, as the transposed view, but most tiles keep the own view's row-order boxes).
+  // The same bits.  CTA pairs need an even number of own-view tiles (N x ceil(W/8) x
+  // floor(H/16)).
+  bool mixed = false;
 };
 // The 3x3 default: halo reuse with 8 x 16 tiles.
 inline Conv3x3Tiling halo_tiling() {
@@ -140,6 +147,18 @@ inline bool halo_transpose_pays(int H, int W) {
   const long long trans = static_cast<long long>((H + 7) / 8) * ((W + 15) / 16);
   return trans < plain;
 }
+// Whether the mixed tiling applies to N images of H x W (pair: on CTA pairs) and needs fewer
+// halo tiles than the map's own view, and no more than the transposed view.
+inline bool halo_mixed_pays(int N, int H, int W, bool pair) {
+  const int rem = H % 16;
+  if (H < 16 || rem == 0 || rem > 8) return false;
+  const long long own_rows = static_cast<long long>((W + 7) / 8) * (H / 16);
+  if (pair && (own_rows * N) % 2 != 0) return false;
+  const long long mixed = own_rows + (W + 15) / 16;
+  const long long plain = static_cast<long long>((W + 7) / 8) * ((H + 15) / 16);
+  const long long trans = static_cast<long long>((H + 7) / 8) * ((W + 15) / 16);
+  return mixed < plain && mixed <= trans;
+}
 inline Conv3x3Tiling halo_pair_tiling() {
   Conv3x3Tiling t = halo_tiling();
   t.pair = true;
@@ -154,6 +173,9 @@ struct TcPlan {
   alignas(64) CUtensorMap map_b;
   alignas(64) CUtensorMap map_out;
   alignas(64) CUtensorMap map_coarse;
+  // halo 3x3 with a mixed tiling: input and output maps of the strip's transposed view
+  alignas(64) CUtensorMap map_a2;
+  alignas(64) CUtensorMap map_out2;
   unsigned char args[256];  // TcGemmArgs, opaque outside tc_kernels.cu
   int mode = 0;  // 0 lateral, 1 conv3x3, 2 conv3x3 halo, 3 halo on CTA pairs, 4 the same + e4m3
                  // quantisation of a bf16 input in shared memory, 5 lateral on CTA pairs,

@@ -171,6 +171,10 @@ int ufpn_core_set_schedule_options(ufpn_core* core, int programmatic_launch, int
  *   "conv3x3_transpose"  0/1  (default 1) halo 3x3s run on the map's transposed view (16 x 8
  *                            tiles) where that needs fewer tiles (200 x 304: 475 instead of
  *                            494 per image); the same bits
+ *   "conv3x3_mixed"      0/1  (default 1) with conv3x3_transpose: the map's own view for its
+ *                            whole 16-row tile rows and the transposed view for the last
+ *                            1..8 rows, where that needs no more tiles than the transposed
+ *                            view (200 x 304: 456 + 19 tiles); the same bits
  *   "conv3x3_dynamic"    0/1  (default 0) 3x3s on CTA pairs claim their work items at run
  *                            time (a device counter) instead of a static round robin; the
  *                            same bits
@@ -254,8 +258,10 @@ int ufpn_lateral_conv_pair(int dtype, const void* x, const void* w, const float*
  * and shared by the nine taps); -1 = the same tiles on CTA pairs (tcgen05 cta_group::2:
  * two SMs share one M = 256 MMA stream and each streams half of the weights); -2 / -3 =
  * 0 / -1 on the map's transposed view (tiles of 16 columns x 8 rows: fewer tiles where H is
- * not a multiple of 16 but W is; the same bits; no P6); 8..128 = plain tiles of that width
- * (one box per tap). */
+ * not a multiple of 16 but W is; the same bits; no P6); -4 / -5 = 0 / -1 with a mixed tiling
+ * (the own view for the whole 16-row tile rows, the transposed view for the remaining 1..8
+ * rows; H % 16 in 1..8; on CTA pairs N x ceil(W/8) x floor(H/16) even; no P6); 8..128 =
+ * plain tiles of that width (one box per tap). */
 int ufpn_conv3x3(int dtype, const void* x, const void* w, const float* bias, void* out,
                  void* p6, int N, int H, int W, int tile_w, void* stream);
 /* ufpn_conv3x3 with an output activation fused into its epilogue after the bias (P6, if
@@ -428,8 +434,8 @@ int ufpn_lateral_conv_e4m3(const void* x, const float* x_scale, int x_scale_per_
                            const void* coarse, void* out, int N, int Cin, int H, int W, int Hc,
                            int Wc, unsigned* amax_out, void* stream);
 /* FP8 3x3 pad-1 conv 256 -> 256 (8 x 16 halo tiles; tile_w -1: on CTA pairs, -2 / -3: the
- * map's transposed view, as for ufpn_conv3x3), NHWC: x e4m3 [N][H][W][256] with device
- * scale(s) as above; w e4m3 packed [256][9][256] (ufpn_quantize_e4m3_rows with pack_cin =
+ * map's transposed view, -4 / -5: mixed, as for ufpn_conv3x3), NHWC: x e4m3 [N][H][W][256]
+ * with device scale(s) as above; w e4m3 packed [256][9][256] (ufpn_quantize_e4m3_rows with pack_cin =
  * 256) with scales [256]; out (and optional p6 = out[::2, ::2]) bf16; amax_out as above.
  * Same role as launch_output_conv (fpn_engine.cu:315-362). */
 int ufpn_conv3x3_e4m3(const void* x, const float* x_scale, int x_scale_per_image, const void* w,

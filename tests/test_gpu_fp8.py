@@ -143,8 +143,8 @@ def test_conv3x3_fp8_matches_oracle(cuda_device, shape, per_image):
 
 @pytest.mark.parametrize("shape", [(3, 13, 21), (2, 37, 50), (1, 200, 304)])
 def test_conv3x3_fp8_transposed_view_equals_plain(cuda_device, shape):
-    """e4m3 3x3 halo tiles on the map's transposed view (tile_w -2, and -3 on CTA pairs) give
-    bitwise the plain halo tiles' results."""
+    """e4m3 3x3 halo tiles on the map's transposed view (tile_w -2, and -3 on CTA pairs) and
+    with the mixed tiling (-4, -5) give bitwise the plain halo tiles' results."""
     import unified_fpn as U
     N, H, W = shape
     g = torch.Generator(device="cuda").manual_seed(16)
@@ -153,7 +153,9 @@ def test_conv3x3_fp8_transposed_view_equals_plain(cuda_device, shape):
     b = (torch.rand(256, device="cuda", generator=g) * 2 - 1) * 0.1
     qw, sw = U.quantize_fp8_rows(w3, pack3x3=True)
     qm, sm = U.quantize_fp8(m, per_image=True)
-    ys = [U.fpn_conv3x3_fp8(qm, sm, qw, sw, b, tile_w=t) for t in (0, -2, -1, -3)]
+    mixed = [-4, -5] if H >= 16 and 0 < H % 16 <= 8 and (N * ((W + 7) // 8) * (H // 16)) % 2 == 0 \
+        else []
+    ys = [U.fpn_conv3x3_fp8(qm, sm, qw, sw, b, tile_w=t) for t in [0, -2, -1, -3] + mixed]
     torch.cuda.synchronize()
     assert U.device_status() == 0
     assert all(torch.equal(ys[0], y) for y in ys[1:])

@@ -295,16 +295,27 @@ def test_conv3x3_cta_pair_equals_single(cuda_device, dtype, shape):
         O.check_close(y2.cpu(), ref, dtype)
 
 
+def _mixed_forms(n, h, w_):
+    """tile_w codes of the mixed tiling that apply to n x h x w_ (-4 single CTA, -5 pairs)."""
+    if h < 16 or h % 16 == 0 or h % 16 > 8:
+        return []
+    own = n * ((w_ + 7) // 8) * (h // 16)
+    return [-4] + ([-5] if own % 2 == 0 else [])
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("shape", [(1, 16, 8), (1, 8, 16), (1, 13, 21), (3, 17, 5), (1, 1, 1),
-                                   (2, 37, 50), (1, 200, 334), (2, 200, 304)])
+                                   (2, 37, 50), (1, 200, 334), (2, 200, 304), (1, 24, 9)])
 def test_conv3x3_transposed_view_equals_plain(cuda_device, dtype, shape):
     """Halo tiles on the map's transposed view (tile_w -2 on single CTAs, -3 on CTA pairs:
     16 columns x 8 rows per tile through tensor maps with the two axes swapped, each tap's
-    halo shift mirrored) give bitwise the results of the plain halo tiles, and match the
-    oracle.  Ragged edges fall on the other axis than with plain tiles.  (2, 200, 304), the
-    R50 P2 map: 950 tiles instead of 988, i.e. 475 pair units on 74 pairs whose last 31 run
-    as channel halves."""
+    halo shift mirrored) and the mixed tiling (-4 / -5: the own view for the whole 16-row
+    tile rows, the transposed view for the last 1..8 rows, where it applies) give bitwise the
+    results of the plain halo tiles, and match the oracle.  Ragged edges fall on other axes
+    than with plain tiles.  (2, 200, 304), the R50 P2 map: 950 tiles instead of 988 either
+    way (mixed: 912 own-view + 38 strip tiles), 475 pair units on 74 pairs whose last 31 run
+    as channel halves.  (3, 17, 5): an odd own-view count, single CTAs only; (1, 24, 9): an
+    odd one on pairs too."""
     import unified_fpn as U
     n, h, w_ = shape
     g = torch.Generator().manual_seed(h * 37 + w_)
@@ -314,7 +325,7 @@ def test_conv3x3_transposed_view_equals_plain(cuda_device, dtype, shape):
     xd = _cl(x.to(cuda_device))
     wp = U.pack_conv3x3_weight(w.to(cuda_device), dtype)
     bd = b.to(cuda_device)
-    ys = [U.fpn_conv3x3(xd, wp, bd, tile_w=t) for t in (0, -2, -1, -3)]
+    ys = [U.fpn_conv3x3(xd, wp, bd, tile_w=t) for t in [0, -2, -1, -3] + _mixed_forms(n, h, w_)]
     torch.cuda.synchronize()
     assert U.device_status() == 0
     assert all(torch.equal(ys[0], y) for y in ys[1:])
@@ -329,17 +340,25 @@ def test_conv3x3_transposed_view_equals_plain(cuda_device, dtype, shape):
 
 
 def test_conv3x3_transposed_view_refuses_p6(cuda_device):
-    """The fused P6 output indexes the map's own rows: the transposed view refuses it on the
-    host (no launch)."""
+    """The fused P6 output indexes the map's own rows: the transposed view and the mixed
+    tiling refuse it on the host (no launch), as the mixed tiling refuses maps it does not
+    apply to."""
     import unified_fpn as U
     x = _cl(torch.randn(1, 256, 8, 8, device=cuda_device).to(torch.bfloat16))
     w = U.pack_conv3x3_weight(torch.randn(256, 256, 3, 3, device=cuda_device), torch.bfloat16)
     b = torch.zeros(256, device=cuda_device)
-    for t in (-2, -3):
+    for t in (-2, -3, -4, -5):
         with pytest.raises(Exception):
             U.fpn_conv3x3(x, w, b, p6=True, tile_w=t)
     with pytest.raises(Exception):
-        U.fpn_conv3x3(x, w, b, tile_w=-4)
+        U.fpn_conv3x3(x, w, b, tile_w=-6)
+    # the mixed tiling needs 1..8 rows past the last whole 16-row tile row, and on CTA pairs
+    # an even number of own-view tiles
+    for shape, t in (((1, 256, 32, 8), -4), ((1, 256, 8, 8), -4), ((1, 256, 28, 8), -4),
+                     ((3, 256, 17, 5), -5)):
+        xs = _cl(torch.randn(*shape, device=cuda_device).to(torch.bfloat16))
+        with pytest.raises(Exception):
+            U.fpn_conv3x3(xs, w, b, tile_w=t)
     assert U.device_status() == 0
 
 

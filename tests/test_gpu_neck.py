@@ -394,14 +394,14 @@ RAGGED = [(52, 70), (26, 35), (13, 18), (7, 9)]
     {"p2_lateral_dynamic": 1, "p2_lateral_ctas": 37}, {"grouped_laterals_pair": 1},
     {"grouped_laterals_pair": 1, "merge_two_levels": 1},
     {"grouped_laterals_pair": 0, "nsplit_p5": 2, "nsplit_p4": 2, "nsplit_p3": 2},
-    {"conv3x3_dynamic": 1}, {"conv3x3_transpose": 0},
+    {"conv3x3_dynamic": 1}, {"conv3x3_transpose": 0}, {"conv3x3_mixed": 0},
     {"conv3x3_p3": -1, "conv3x3_p4": -1, "conv3x3_p5": -1},
     {"conv3x3_p3": -1, "conv3x3_p4": -1, "conv3x3_p5": -1, "conv3x3_dynamic": 1},
     {"merge_units": -1},
 ], ids=["split", "fused", "grouped_topdown", "ksplit", "topdown_ksplit", "merge_two_levels",
         "nsplit", "topdown_nsplit", "nsplit_ksplit", "p2_dynamic", "p2_dynamic_37ctas",
         "lateral_pairs", "lateral_pairs_two_level", "nsplit_single_cta", "conv_claims",
-        "conv_plain_view", "conv_pairs_all_levels", "conv_pairs_all_levels_claims",
+        "conv_plain_view", "conv_transposed_view", "conv_pairs_all_levels", "conv_pairs_all_levels_claims",
         "merge_warp_per_pixel"])
 def test_neck_ragged_tile_seams(cuda_device, opts):
     """Every schedule option on ragged maps against the oracle (max-norm and per-element),
@@ -487,12 +487,13 @@ def test_grouped_lateral_variants_equal_whole_tiles_bitwise(cuda_device, variant
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_conv3x3_tail_halves_bitwise_at_full_size(cuda_device, dtype):
     """At the R50 800x1216 batch-2 workload the merges run one warp per 8-pixel unit (the
-    default; merge_units = -1: one warp per pixel) and the 3x3s tile the P2 / P3 / P4 maps on their
-    transposed views (conv3x3_transpose, the default: 950 / 260 / 70 tiles instead of 988 /
-    266 / 80), and the P2 3x3 on CTA pairs then ends with 31 of 475 pair units on 74 pairs,
-    run as channel halves (conv3x3_tail_halves, the default).  The neck is bitwise what plain
-    tiles, whole units and run-time item claims (conv3x3_dynamic) give, and matches the
-    oracle."""
+    default; merge_units = -1: one warp per pixel) and the 3x3s tile the P2 / P3 / P4 maps
+    with mixed tilings (the own view for whole 16-row tile rows, the transposed view for the
+    rest: 950 / 248 / 70 tiles instead of 988 / 266 / 80; conv3x3_mixed = 0: the transposed
+    views, 950 / 260 / 70), and the P2 3x3 on CTA pairs then ends with 31 of 475 pair units on
+    74 pairs, run as channel halves (conv3x3_tail_halves, the default).  The neck is bitwise
+    what plain tiles, whole units and run-time item claims (conv3x3_dynamic) give, and matches
+    the oracle."""
     import unified_fpn as U
     sizes = O.level_sizes(800, 1216)
     host = O.make_features(2, O.R50_CHANNELS, sizes, seed=95)
@@ -501,6 +502,7 @@ def test_conv3x3_tail_halves_bitwise_at_full_size(cuda_device, dtype):
     res = []
     for opts in ({}, {"conv3x3_tail_halves": 0}, {"conv3x3_transpose": 0},
                  {"conv3x3_tail_halves": 0, "conv3x3_transpose": 0}, {"conv3x3_dynamic": 1},
+                 {"conv3x3_mixed": 0},
                  {"merge_units": -1}):
         fpn = U.UnifiedFPN()
         for k, v in opts.items():
