@@ -199,6 +199,7 @@ struct UnifiedFPNCore::Impl {
   bool p2_pair = false;         // 16-bit P2 lateral on CTA pairs (resident weight halves)
   int merge_units = 0;  // merge kernel form / units per block (launch_upsample_add)
   int p2_lateral_ctas = 0;      // CTAs of the 16-bit P2 lateral (0: one per SM)
+  int conv_ctas[4] = {0, 0, 0, 0};  // CTAs of each level's 3x3 (0: one per SM)
   bool p2_lateral_dynamic = false;  // 16-bit P2 lateral as a one-job neck launch (tile claims)
   // Options set through UnifiedFPNCore::set_option, by name, re-applied after every
   // (re)configuration so that a choice made before the first forward -- or kept across a new
@@ -648,7 +649,7 @@ struct UnifiedFPNCore::Impl {
       check(ufpn::plan_tc_conv3x3(conv, dtype, merged[l], out_wp[l], out_b[l], o[l], p6_out,
                                   batch, H[l], W[l],
                                   conv_tiling_for(l, tiling_for(l), p6_out != nullptr, batch),
-                                  d_status, 0, act_scales(), conv_claim(l)),
+                                  d_status, conv_ctas[l], act_scales(), conv_claim(l)),
             "plan conv3x3");
       // (on the main stream the 3x3 follows a kernel: the P2 lateral, or the previous
       // level's merge / 3x3 when every kernel runs on one stream)
@@ -921,7 +922,7 @@ struct UnifiedFPNCore::Impl {
       TcPlan conv;
       check(ufpn::plan_tc_conv3x3(conv, DType::E4M3, in_kernel ? merged[l] : qmerged[l],
                                   out_wp[l], out_b[l], out[l], l == 3 ? p6 : nullptr, batch,
-                                  H[l], W[l], t, d_status, 0, sc, conv_claim(l)),
+                                  H[l], W[l], t, d_status, conv_ctas[l], sc, conv_claim(l)),
             "plan e4m3 conv3x3");
       ok(ufpn::launch_tc(conv, conv_st,
                          opts(pdl && (conv_st == main || (quantise && !in_kernel)))),
@@ -1106,6 +1107,12 @@ void UnifiedFPNCore::configure_levels(const std::vector<FPNDimensions>& dims, in
                                                                         m.lat_tiling[0]));
     const int sms = ufpn::sm_count();
     m.p2_lateral_ctas = (lt >= 4LL * sms && lt <= 10LL * sms) ? sms * 128 / 148 : 0;
+    // e4m3: the P3 3x3 (on CTA pairs, beside the P2 lateral's tail) on 96 of 148 SMs, so
+    // that the quantisation pass over M2, which the P2 3x3 waits for, gets SMs as soon as
+    // the P2 lateral ends (R50 640x640 x 16: -3.5..-5 %; its blocks did not start beside
+    // the pair CTAs and waited ~40 us for them).
+    for (int l = 0; l < 4; ++l) m.conv_ctas[l] = 0;
+    if (dt == DType::E4M3) m.conv_ctas[1] = sms * 96 / 148;
   }
   m.p2_lateral_dynamic = false;
   m.apply_tuning_db2();         // a whole-neck tuning of this geometry, if any
@@ -1529,6 +1536,13 @@ const std::vector<EngineOption>& engine_options() {
     o.push_back({"p2_lateral_ctas", [](int v) { return v >= 0 && v <= 4096; },
                  [](UnifiedFPNCore::Impl& m, int v) { m.p2_lateral_ctas = v; },
                  [](const UnifiedFPNCore::Impl& m) { return m.p2_lateral_ctas; }});
+    for (int l = 0; l < 4; ++l) {
+      static const char* names[4] = {"conv3x3_ctas_p2", "conv3x3_ctas_p3", "conv3x3_ctas_p4",
+                                     "conv3x3_ctas_p5"};
+      o.push_back({names[l], [](int v) { return v >= 0 && v <= 4096; },
+                   [l](UnifiedFPNCore::Impl& m, int v) { m.conv_ctas[l] = v; },
+                   [l](const UnifiedFPNCore::Impl& m) { return m.conv_ctas[l]; }});
+    }
     o.push_back({"merge_units", [](int v) { return v >= -1 && v <= 256; },
                  [](UnifiedFPNCore::Impl& m, int v) { m.merge_units = v; },
                  [](const UnifiedFPNCore::Impl& m) { return m.merge_units; }});
@@ -1654,6 +1668,13 @@ std::string UnifiedFPNCore::autotune(const void* const* in, void* const* out, vo
   } else {
     knobs.push_back({"fp8_two_pass_p2", {0, 1}});
     knobs.push_back({"fp8_quantise_in_conv", {0, 1}});
+  }
+  {
+    const int sms = ufpn::sm_count();
+    Knob k{"conv3x3_ctas_p3", {m.conv_ctas[1]}};
+    for (int v : {0, sms * 80 / 148, sms * 96 / 148, sms * 112 / 148})
+      if (std::find(k.values.begin(), k.values.end(), v) == k.values.end()) k.values.push_back(v);
+    knobs.push_back(k);
   }
   knobs.push_back({"conv3x3_transpose", {1, 0}});
   knobs.push_back({"conv3x3_mixed", {1, 0}});

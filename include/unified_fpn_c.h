@@ -171,6 +171,10 @@ int ufpn_core_set_schedule_options(ufpn_core* core, int programmatic_launch, int
  *   "conv3x3_transpose"  0/1  (default 1) halo 3x3s run on the map's transposed view (16 x 8
  *                            tiles) where that needs fewer tiles (200 x 304: 475 instead of
  *                            494 per image); the same bits
+ *   "conv3x3_ctas_p2" .. "conv3x3_ctas_p5"  0..4096  CTAs of that level's 3x3 (0 = one per
+ *                            SM; a CTA-pair 3x3 takes pairs of them).  Default 0, except the
+ *                            e4m3 P3 3x3 on 96/148 of the SMs (the quantisation of M2 then
+ *                            starts beside it as soon as the P2 lateral ends)
  *   "conv3x3_mixed"      0/1  (default 1) with conv3x3_transpose: the map's own view for its
  *                            whole 16-row tile rows and the transposed view for the last
  *                            1..8 rows, where that needs no more tiles than the transposed

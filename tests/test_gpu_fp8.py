@@ -309,15 +309,17 @@ def test_fp8_neck_transposed_view_and_claims_are_bitwise_equal(cuda_device):
     their transposed views by default (143 instead of 147 tiles at 100 x 167): bitwise what
     plain tiles give, and what CTA-pair 3x3s that claim their items at run time give, with the
     separate quantisation pass and with the 3x3 that quantises its input itself, repeated
-    launches included (the claim counters reset themselves); and the merges (with their
-    per-image absmax and scaled copy) one warp per pixel instead of per 8-pixel unit."""
+    launches included (the claim counters reset themselves); the merges (with their
+    per-image absmax and scaled copy) one warp per pixel instead of per 8-pixel unit; and the
+    3x3s on other CTA counts (the P3 3x3 on all SMs instead of its e4m3 default of 96/148,
+    the P2 3x3 on 60)."""
     import unified_fpn as U
     chans, sizes = O.SWIN_CHANNELS, [(100, 167), (50, 84), (25, 42), (13, 21)]
     _, wts, qf, sc = _fp8_case(2, chans, sizes, seed=43)
     outs = []
     for opts in ({}, {"conv3x3_transpose": 0}, {"conv3x3_dynamic": 1},
                  {"fp8_quantise_in_conv": 1}, {"fp8_quantise_in_conv": 1, "conv3x3_dynamic": 1},
-                 {"merge_units": -1}):
+                 {"merge_units": -1}, {"conv3x3_ctas_p3": 0}, {"conv3x3_ctas_p2": 60}):
         fpn = U.UnifiedFPN()
         for k, v in opts.items():
             fpn.set_option(k, v)

@@ -397,12 +397,12 @@ RAGGED = [(52, 70), (26, 35), (13, 18), (7, 9)]
     {"conv3x3_dynamic": 1}, {"conv3x3_transpose": 0}, {"conv3x3_mixed": 0},
     {"conv3x3_p3": -1, "conv3x3_p4": -1, "conv3x3_p5": -1},
     {"conv3x3_p3": -1, "conv3x3_p4": -1, "conv3x3_p5": -1, "conv3x3_dynamic": 1},
-    {"merge_units": -1},
+    {"merge_units": -1}, {"conv3x3_ctas_p3": 40, "conv3x3_ctas_p2": 64, "conv3x3_ctas_p4": 9},
 ], ids=["split", "fused", "grouped_topdown", "ksplit", "topdown_ksplit", "merge_two_levels",
         "nsplit", "topdown_nsplit", "nsplit_ksplit", "p2_dynamic", "p2_dynamic_37ctas",
         "lateral_pairs", "lateral_pairs_two_level", "nsplit_single_cta", "conv_claims",
         "conv_plain_view", "conv_transposed_view", "conv_pairs_all_levels", "conv_pairs_all_levels_claims",
-        "merge_warp_per_pixel"])
+        "merge_warp_per_pixel", "conv_cta_caps"])
 def test_neck_ragged_tile_seams(cuda_device, opts):
     """Every schedule option on ragged maps against the oracle (max-norm and per-element),
     bitwise deterministic, and each image alone equals its slice of the batch."""
@@ -526,6 +526,7 @@ def test_options_set_before_the_first_forward_survive_configuration(cuda_device)
     with them must still match the oracle."""
     import unified_fpn as U
     chosen = {"p2_lateral_dynamic": 1, "merge_units": 4, "conv3x3_p3": 16, "lateral_tile_p2": 8,
+              "conv3x3_ctas_p3": 50,
               "p2_lateral_ctas": 100}
     fpn = U.UnifiedFPN()
     for k, v in chosen.items():
