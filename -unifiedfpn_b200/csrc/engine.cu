@@ -1082,9 +1082,13 @@ void UnifiedFPNCore::configure_levels(const std::vector<FPNDimensions>& dims, in
     m.H[l] = dims[l].height;
     m.W[l] = dims[l].width;
     // CTA pairs pay off on large maps only (measured: single-CTA halo tiles are faster up
-    // to a few hundred tiles, where the pair's longer fill and tail dominate).
+    // to a few hundred tiles, where the pair's longer fill and tail dominate), and not for
+    // the P2 3x3: its CTAs enter as the P2 lateral and the side 3x3s free SMs, and single
+    // CTAs take any SM that frees while a pair needs both SMs of a TPC (R50 800x1216 x 2 / x 4,
+    // 1024^2 x 8, Swin 1333x800 x 8: 3-4.5 % faster end to end than pairs, paired A/Bs).
     const long long tiles = static_cast<long long>(N) * ((m.H[l] + 15) / 16) * ((m.W[l] + 7) / 8);
-    m.tiling[l] = tiling_from_code(tiles >= 4LL * ufpn::sm_count() ? kDefaultTilingCode : 0);
+    m.tiling[l] =
+        tiling_from_code(l > 0 && tiles >= 4LL * ufpn::sm_count() ? kDefaultTilingCode : 0);
     m.tiling_tuned[l] = false;
     auto it = m.tuning_db.find(m.tuning_key(l));
     if (it != m.tuning_db.end()) {
@@ -1098,15 +1102,13 @@ void UnifiedFPNCore::configure_levels(const std::vector<FPNDimensions>& dims, in
   }
   m.p2_pair = false;
   m.merge_units = 0;
-  // A short P2 lateral (4..10 tiles per SM) on 128 of 148 SMs: the P3 / P4 3x3s then run
-  // beside it instead of waiting for its CTAs (R50 800x1216 x 2, 6.4 tiles per SM: -2.8 %
-  // end to end, same-box A/B).  Longer ones (R50 1024^2 x 8, Swin 1333x800 x 8: 28 tiles per
-  // SM) lose throughput with fewer CTAs, shorter ones (x 1, 3.2) measured no difference.
+  // The P2 lateral on every SM.  (With the P2 3x3 on CTA pairs, a short P2 lateral -- 4..10
+  // tiles per SM -- ran best on 128 of 148 SMs, so that the P3 / P4 3x3s could run beside
+  // it; with the P2 3x3 on single CTAs, whose tiles fill any SM the lateral frees, all SMs
+  // are 0.6-1.2 % faster.  The option and the autotuner keep the cap.)
   {
-    const long long lt = static_cast<long long>(ufpn::neck_lateral_tiles(N, m.H[0], m.W[0],
-                                                                        m.lat_tiling[0]));
     const int sms = ufpn::sm_count();
-    m.p2_lateral_ctas = (lt >= 4LL * sms && lt <= 10LL * sms) ? sms * 128 / 148 : 0;
+    m.p2_lateral_ctas = 0;
     // e4m3: the P3 3x3 (on CTA pairs, beside the P2 lateral's tail) on 96 of 148 SMs, so
     // that the quantisation pass over M2, which the P2 3x3 waits for, gets SMs as soon as
     // the P2 lateral ends (R50 640x640 x 16: -3.5..-5 %; its blocks did not start beside

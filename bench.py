@@ -727,16 +727,16 @@ def main():
             memory_format=torch.channels_last)
         w3 = torch.randn(256, 256, 3, 3, device=dev, generator=gen) * 0.03
         bias = torch.zeros(256, device=dev)
-        # the engine's form: halo tiles on CTA pairs, with the mixed tiling (tile_w -5: the own
+        # the engine's form: single-CTA halo tiles, with the mixed tiling (tile_w -4: the own
         # view for whole 16-row tile rows, the transposed view for the last 1..8 rows) or the
-        # transposed view (-3) when that needs fewer 8 x 16 tiles (200 x 304: 475 instead of 494
+        # transposed view (-2) when that needs fewer 8 x 16 tiles (200 x 304: 475 instead of 494
         # per image)
         plain_tiles = -(-w2 // 8) * -(-h2 // 16)
         trans_tiles = -(-h2 // 8) * -(-w2 // 16)
         mixed_tiles = -(-w2 // 8) * (h2 // 16) + -(-w2 // 16)
-        mixed_ok = (h2 >= 16 and 0 < h2 % 16 <= 8 and (B * -(-w2 // 8) * (h2 // 16)) % 2 == 0
+        mixed_ok = (h2 >= 16 and 0 < h2 % 16 <= 8
                     and mixed_tiles < plain_tiles and mixed_tiles <= trans_tiles)
-        tw = -5 if mixed_ok else (-3 if trans_tiles < plain_tiles else -1)
+        tw = -4 if mixed_ok else (-2 if trans_tiles < plain_tiles else 0)
         if fp8:
             xq, xs = U.quantize_fp8(xr, per_image=True)
             wq, wsc = U.quantize_fp8_rows(w3, pack3x3=True)
@@ -764,9 +764,11 @@ def main():
         peak = peaks["bf16_tflops"] * mult
         traffic = profile_traffic("conv3x3_fp8_p2_r50_640x640_b16" if fp8
                                   else "conv3x3_p2_r50_800x1216_b2")
-        # the engine's 3x3: halo tiles on CTA pairs (tcgen05 cta_group::2)
-        roofline = {"kernel": f"conv3x3 P2 implicit GEMM (tcgen05 cta_group::2 "
-                              f"{'kind::f8f6f4' if fp8 else 'kind::f16'}), {B}x{h2}x{w2}x256 -> 256",
+        # the engine's P2 3x3: single-CTA halo tiles (tcgen05, TMEM accumulators)
+        form = {-4: "mixed tiling", -2: "transposed view", 0: "own view"}[tw]
+        roofline = {"kernel": f"conv3x3 P2 implicit GEMM (tcgen05 "
+                              f"{'kind::f8f6f4' if fp8 else 'kind::f16'}, halo tiles, {form}), "
+                              f"{B}x{h2}x{w2}x256 -> 256",
                     "bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
                     "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                     "peak_src": (f"derived: 2 x {peaks['src']} bf16 burst" if fp8
