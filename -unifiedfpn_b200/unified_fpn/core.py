@@ -59,7 +59,9 @@ class UnifiedFPN:
 
     def __del__(self):
         h = getattr(self, "_h", None)
-        if h is not None and h.value:
+        # (at interpreter exit the module globals may already be cleared: the process's
+        # teardown then releases the engine with the CUDA context)
+        if h is not None and h.value and lib is not None:
             lib.ufpn_core_destroy(h)
             self._h = None
 
