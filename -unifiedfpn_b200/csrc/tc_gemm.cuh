@@ -545,7 +545,9 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
   uint32_t acc_phase = 0;
   const int rank = kPair ? static_cast<int>(cluster_ctarank()) : 0;
   const int units = kPair ? (args.num_tiles + 1) / 2 : args.num_tiles;
-  const int items = kPair ? units + args.pair_tail : units;
+  // (3x3: the last pair_tail units -- pair units, or tiles on single CTAs -- run as two
+  // channel-half items each; 0 for the laterals)
+  const int items = units + args.pair_tail;
   const int ustep = kPair ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
   // (kPair with a claim ring: the items in the order the leader claimed them)
   for (int it = kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);;
@@ -555,7 +557,7 @@ __device__ __forceinline__ void tc_epilogue(const TcGemmArgs& args, const CUtens
       break;
     if (it >= items) break;
     int half = -1;  // channel-half item of a CTA-pair 3x3 (its accumulator has N = 128)
-    const int u = kPair ? pair_item_unit(args, units, it, half) : it;
+    const int u = pair_item_unit(args, units, it, half);
     const int tile = kPair ? 2 * u + rank : u;
     const bool real = tile < args.num_tiles;
     const bool ok =
@@ -1073,7 +1075,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                             const __grid_constant__ CUtensorMap map_b,
                             const __grid_constant__ CUtensorMap map_out,
                             const __grid_constant__ CUtensorMap map_a2,
-                            const __grid_constant__ CUtensorMap map_out2, const TcGemmArgs args) {
+                            const __grid_constant__ CUtensorMap map_out2,
+                            const __grid_constant__ CUtensorMap map_bh, const TcGemmArgs args) {
   constexpr int S = kHaloStages;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -1119,6 +1122,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       prefetch_tmap(&map_a2);
       prefetch_tmap(&map_out2);
     }
+    if (args.pair_tail > 0) prefetch_tmap(&map_bh);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTcTmemCols);
@@ -1136,10 +1140,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       int stage = 0, hb = 0, issued = 0, hissued = 0;
       uint32_t phase = 0, hphase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < args.num_tiles; tile += gridDim.x) {
+      // items: tiles, the last pair_tail of them as two channel halves each (N = 128 items
+      // load 128 weight rows through map_bh)
+      const int items = args.num_tiles + args.pair_tail;
+      for (int it = blockIdx.x; ok && it < items; it += gridDim.x) {
+        int half;
+        const int tile = pair_item_unit(args, args.num_tiles, it, half);
         const HaloTile ht = halo_tile(args, tile);
         const int n = ht.n, x0 = ht.x0, y0 = ht.y0;
         const CUtensorMap* ma = ht.strip ? &map_a2 : &map_a;
+        const CUtensorMap* mb = half < 0 ? &map_b : &map_bh;
+        const uint32_t bbytes = half < 0 ? kTcBStage : kTcBStage / 2;
+        const int brow = half < 0 ? 0 : half * (kTcBlockN / 2);
         for (int cb = 0; ok && cb < cin_blocks; ++cb) {
           if (!mbar_wait(&hempty_bar[hb], hphase ^ 1u, abort_flag, args.status,
                          kDevTimeoutProducer)) {
@@ -1160,9 +1172,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(&full_bar[stage], kTcBStage);
-            tma_load_2d(smem_b + stage * kTcBStage, &map_b, &full_bar[stage],
-                        (tap * cin_blocks + cb) * kKbElems<T>, 0, kPolicyEvictLast);
+            mbar_arrive_expect_tx(&full_bar[stage], bbytes);
+            tma_load_2d(smem_b + stage * kTcBStage, mb, &full_bar[stage],
+                        (tap * cin_blocks + cb) * kKbElems<T>, brow, kPolicyEvictLast);
             ++issued;
             if (++stage == S) {
               stage = 0;
@@ -1190,12 +1202,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc =
+      constexpr uint32_t idesc_full =
           make_idesc(kTcBlockM, kTcBlockN, TcElem<T>::kFmt, TcElem<T>::kFmt);
+      constexpr uint32_t idesc_half =
+          make_idesc(kTcBlockM, kTcBlockN / 2, TcElem<T>::kFmt, TcElem<T>::kFmt);
       int stage = 0, hb = 0, acc = 0;
       uint32_t phase = 0, hphase = 0, acc_phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < args.num_tiles; tile += gridDim.x) {
+      const int items = args.num_tiles + args.pair_tail;
+      for (int it = blockIdx.x; ok && it < items; it += gridDim.x) {
+        int half;
+        const int tile = pair_item_unit(args, args.num_tiles, it, half);
+        const uint32_t idesc = half < 0 ? idesc_full : idesc_half;
         if (!mbar_wait(&acce_bar[acc], acc_phase ^ 1u, abort_flag, args.status, kDevTimeoutMma))
           break;
         tc_fence_after();

@@ -170,9 +170,10 @@ cudaError_t launch_halo_t(const TcPlan& p, cudaStream_t s, LaunchOpts opts) {
   if (e != cudaSuccess) return e;
   TcGemmArgs a;
   std::memcpy(&a, p.args, sizeof(a));
+  // (map_coarse of a single-CTA halo plan: the 128-row weight box of its channel-half items)
   return launch_ex(fpn_conv3x3_halo_kernel<T>, dim3(p.grid), dim3(kTcThreads),
                    HaloCfg::kSmemBytes, s, opts, 1, p.map_a, p.map_b, p.map_out, p.map_a2,
-                   p.map_out2, a);
+                   p.map_out2, p.map_coarse, a);
 }
 
 template <typename T, bool kCvt, bool kClaims>
@@ -458,6 +459,14 @@ cudaError_t plan_tc_conv3x3(TcPlan& plan, DType dt, const void* x, const void* w
     }
   } else {
     plan.grid = a.num_tiles < cap ? a.num_tiles : cap;
+    // Halo tiles on single CTAs: the same for a last round of rem < grid tiles that fit the
+    // CTAs as halves (2 rem <= grid; the halves' weight box has 128 rows).
+    const int rem = plan.grid > 0 ? a.num_tiles % plan.grid : 0;
+    if (halo && tiling.tail_halves && rem > 0 && 2 * rem <= plan.grid) {
+      a.pair_tail = rem;
+      if ((e = encode_weights(&plan.map_coarse, dt, w, 9 * C, kTcBlockN / 2)) != cudaSuccess)
+        return e;
+    }
   }
   std::memcpy(plan.args, &a, sizeof(a));
   return cudaSuccess;

@@ -314,7 +314,8 @@ def test_conv3x3_transposed_view_equals_plain(cuda_device, dtype, shape):
     results of the plain halo tiles, and match the oracle.  Ragged edges fall on other axes
     than with plain tiles.  (2, 200, 304), the R50 P2 map: 950 tiles instead of 988 either
     way (mixed: 912 own-view + 38 strip tiles), 475 pair units on 74 pairs whose last 31 run
-    as channel halves.  (3, 17, 5): an odd own-view count, single CTAs only; (1, 24, 9): an
+    as channel halves; on single CTAs its last 62 of 950 tiles (100 of 988 on the own view)
+    run as channel halves on 148 SMs.  (3, 17, 5): an odd own-view count, single CTAs only; (1, 24, 9): an
     odd one on pairs too."""
     import unified_fpn as U
     n, h, w_ = shape

@@ -490,9 +490,9 @@ def test_conv3x3_tail_halves_bitwise_at_full_size(cuda_device, dtype):
     default; merge_units = -1: one warp per pixel) and the 3x3s tile the P2 / P3 / P4 maps
     with mixed tilings (the own view for whole 16-row tile rows, the transposed view for the
     rest: 950 / 248 / 70 tiles instead of 988 / 266 / 80; conv3x3_mixed = 0: the transposed
-    views, 950 / 260 / 70), the P2 3x3 on single CTAs.  On CTA pairs (conv3x3_p2 = -1) the P2
-    3x3 ends with 31 of 475 pair units on 74 pairs, run as channel halves
-    (conv3x3_tail_halves, the default).  The neck is bitwise the same with pairs, plain tiles,
+    views, 950 / 260 / 70), the P2 3x3 on single CTAs, whose last 62 of 950 tiles on 148 CTAs
+    run as channel halves (conv3x3_tail_halves, the default).  On CTA pairs (conv3x3_p2 = -1)
+    the P2 3x3 ends with 31 of 475 pair units on 74 pairs, run as channel halves.  The neck is bitwise the same with pairs, plain tiles,
     whole units and run-time item claims (conv3x3_dynamic), and matches the oracle."""
     import unified_fpn as U
     sizes = O.level_sizes(800, 1216)
@@ -500,7 +500,8 @@ def test_conv3x3_tail_halves_bitwise_at_full_size(cuda_device, dtype):
     wts = O.make_weights(O.R50_CHANNELS, seed=96, bias_scale=0.1)
     xin = [_cl(f.to(dtype).cuda()) for f in host]
     res = []
-    for opts in ({}, {"conv3x3_p2": -1}, {"conv3x3_p2": -1, "conv3x3_tail_halves": 0},
+    for opts in ({}, {"conv3x3_tail_halves": 0}, {"conv3x3_p2": -1},
+                 {"conv3x3_p2": -1, "conv3x3_tail_halves": 0},
                  {"conv3x3_transpose": 0},
                  {"conv3x3_p2": -1, "conv3x3_tail_halves": 0, "conv3x3_transpose": 0},
                  {"conv3x3_p2": -1, "conv3x3_dynamic": 1}, {"conv3x3_mixed": 0},
