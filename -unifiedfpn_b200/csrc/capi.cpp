@@ -683,10 +683,10 @@ int conv3x3_backward(int dtype, const void* x, const void* w, const void* w_f,
       wf = base;
     }
     ufpn::TcPlan plan;
-    // halo tiles on CTA pairs, as the forward engine runs its 3x3s (on the map's transposed
-    // view where that needs fewer tiles; the same bits)
-    ufpn::Conv3x3Tiling t = ufpn::halo_pair_tiling();
-    if (ufpn::halo_mixed_pays(N, H, W, true))
+    // single-CTA halo tiles, as the forward engine runs its 3x3s (mixed tiling or the map's
+    // transposed view where that needs fewer tiles; the same bits)
+    ufpn::Conv3x3Tiling t = ufpn::halo_tiling();
+    if (ufpn::halo_mixed_pays(N, H, W, false))
       t.mixed = true;
     else
       t.transposed = ufpn::halo_transpose_pays(H, W);
@@ -792,9 +792,17 @@ int ufpn_neck_train_forward(int dtype, int N, const int* cin, const int* H, cons
                            l < 3 ? H[l + 1] : 0, l < 3 ? W[l + 1] : 0, stream);
     if (rc != UFPN_OK) return rc;
   }
-  for (int l = 0; l < 4; ++l) {  // 3x3s on CTA-pair halo tiles
-    rc = ufpn_conv3x3_act(dtype, merged[l], packed[l], conv_b[l], out[l], l == 3 ? p6 : nullptr, N,
-                          H[l], W[l], -1, 0, 0.01f, stream);
+  for (int l = 0; l < 4; ++l) {
+    // 3x3s on single-CTA halo tiles, with the mixed tiling or the transposed view where that
+    // needs fewer tiles (not with the fused P6): 2-5 % faster per training step than CTA pairs
+    // on the own view
+    const bool with_p6 = l == 3 && p6 != nullptr;
+    const int tw = with_p6 ? 0
+                   : ufpn::halo_mixed_pays(N, H[l], W[l], false)   ? -4
+                   : ufpn::halo_transpose_pays(H[l], W[l])          ? -2
+                                                                    : 0;
+    rc = ufpn_conv3x3_act(dtype, merged[l], packed[l], conv_b[l], out[l], with_p6 ? p6 : nullptr,
+                          N, H[l], W[l], tw, 0, 0.01f, stream);
     if (rc != UFPN_OK) return rc;
   }
   return UFPN_OK;

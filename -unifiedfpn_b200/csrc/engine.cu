@@ -1081,14 +1081,15 @@ void UnifiedFPNCore::configure_levels(const std::vector<FPNDimensions>& dims, in
     m.cin[l] = dims[l].channels;
     m.H[l] = dims[l].height;
     m.W[l] = dims[l].width;
-    // CTA pairs pay off on large maps only (measured: single-CTA halo tiles are faster up
-    // to a few hundred tiles, where the pair's longer fill and tail dominate), and not for
-    // the P2 3x3: its CTAs enter as the P2 lateral and the side 3x3s free SMs, and single
-    // CTAs take any SM that frees while a pair needs both SMs of a TPC (R50 800x1216 x 2 / x 4,
-    // 1024^2 x 8, Swin 1333x800 x 8: 3-4.5 % faster end to end than pairs, paired A/Bs).
+    // Single-CTA halo tiles on every level: their CTAs enter as other kernels free SMs, and a
+    // single CTA takes any SM that frees while a CTA pair needs both SMs of a TPC.  Measured
+    // against pairs on the maps with >= 4 tiles per SM (paired A/Bs): the P2 3x3 3-4.5 %
+    // faster end to end (R50 800x1216 x 2 / x 4, 1024^2 x 8, Swin 1333x800 x 8), the P3 3x3 of
+    // the x 8 workloads another 2-3 %; alone, the two forms time the same.  (e4m3: pairs.)
     const long long tiles = static_cast<long long>(N) * ((m.H[l] + 15) / 16) * ((m.W[l] + 7) / 8);
-    m.tiling[l] =
-        tiling_from_code(l > 0 && tiles >= 4LL * ufpn::sm_count() ? kDefaultTilingCode : 0);
+    m.tiling[l] = tiling_from_code(dt == DType::E4M3 && l > 0 && tiles >= 4LL * ufpn::sm_count()
+                                       ? kDefaultTilingCode
+                                       : 0);
     m.tiling_tuned[l] = false;
     auto it = m.tuning_db.find(m.tuning_key(l));
     if (it != m.tuning_db.end()) {
