@@ -569,6 +569,77 @@ struct StreamScratch {
 bool parse_16bit(int dtype, DType* dt) {
   return parse_dtype(dtype, dt) && (*dt == DType::BF16 || *dt == DType::F16);
 }
+
+// Per-level work of a training step on up to four streams: a LevelFork makes three side
+// streams wait for everything enqueued on `main` so far, hands out a stream per level --
+// P5, P4, P3 on the side streams, P2 (the largest) on `main` -- and, when it goes out of
+// scope, makes `main` wait for the side streams.  The small levels' grids (20-70 CTAs) then
+// share the GPU with the large ones instead of holding it alone; a captured step becomes one
+// graph with the same fork and join.  The side streams and events are made once per device
+// (outside a capture: the first, eager step); if they cannot be made, every level runs on
+// `main`.  One fork at a time per device (its lock is held until the join).
+struct SideStreams {
+  cudaStream_t st[3] = {};
+  cudaEvent_t fork = nullptr;
+  cudaEvent_t join[3] = {};
+  bool ready = false;
+  std::mutex mu;
+};
+SideStreams* side_streams() {
+  static SideStreams per_dev[64];
+  static std::mutex create_mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  SideStreams& ss = per_dev[dev];
+  std::lock_guard<std::mutex> lk(create_mu);
+  if (!ss.ready) {
+    // (relaxed capture mode while creating them, so that a capture elsewhere in the
+    // process does not refuse the calls; the thread's own mode is restored after)
+    cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+    cudaThreadExchangeStreamCaptureMode(&mode);
+    bool ok = true;
+    for (auto& x : ss.st)
+      ok = ok && cudaStreamCreateWithFlags(&x, cudaStreamNonBlocking) == cudaSuccess;
+    ok = ok && cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming) == cudaSuccess;
+    for (auto& e : ss.join)
+      ok = ok && cudaEventCreateWithFlags(&e, cudaEventDisableTiming) == cudaSuccess;
+    cudaThreadExchangeStreamCaptureMode(&mode);
+    if (!ok) {
+      cudaGetLastError();  // (leaves no sticky error; every level then runs on `main`)
+      return nullptr;
+    }
+    ss.ready = true;
+  }
+  return &ss;
+}
+class LevelFork {
+ public:
+  explicit LevelFork(cudaStream_t main) : main_(main), ss_(side_streams()) {
+    if (ss_) {
+      lock_ = std::unique_lock<std::mutex>(ss_->mu);
+      forked_ = cudaEventRecord(ss_->fork, main_) == cudaSuccess;
+      for (int i = 0; forked_ && i < 3; ++i)
+        forked_ = cudaStreamWaitEvent(ss_->st[i], ss_->fork, 0) == cudaSuccess;
+    }
+  }
+  ~LevelFork() {
+    if (!forked_) return;
+    for (int i = 0; i < 3; ++i) {
+      cudaEventRecord(ss_->join[i], ss_->st[i]);
+      cudaStreamWaitEvent(main_, ss_->join[i], 0);
+    }
+  }
+  // level 0..3 = P2..P5
+  void* stream(int level) const {
+    return forked_ && level > 0 ? static_cast<void*>(ss_->st[level - 1]) : static_cast<void*>(main_);
+  }
+
+ private:
+  cudaStream_t main_;
+  SideStreams* ss_;
+  std::unique_lock<std::mutex> lock_;
+  bool forked_ = false;
+};
 }  // namespace
 
 // Zero fp32 bias of the input-gradient launches (2048 floats, enough for Cin = 2048), one per
@@ -792,7 +863,10 @@ int ufpn_neck_train_forward(int dtype, int N, const int* cin, const int* H, cons
                            l < 3 ? H[l + 1] : 0, l < 3 ? W[l + 1] : 0, stream);
     if (rc != UFPN_OK) return rc;
   }
-  for (int l = 0; l < 4; ++l) {
+  // The four 3x3s are independent: P5, P4, P3 on side streams, P2 on the caller's (the side
+  // levels enqueued first, so that their grids get SMs beside the P2 3x3's).
+  LevelFork fork(static_cast<cudaStream_t>(stream));
+  for (int l = 3; l >= 0; --l) {
     // 3x3s on single-CTA halo tiles, with the mixed tiling or the transposed view where that
     // needs fewer tiles (not with the fused P6): 2-5 % faster per training step than CTA pairs
     // on the own view
@@ -802,7 +876,7 @@ int ufpn_neck_train_forward(int dtype, int N, const int* cin, const int* H, cons
                    : ufpn::halo_transpose_pays(H[l], W[l])          ? -2
                                                                     : 0;
     rc = ufpn_conv3x3_act(dtype, merged[l], packed[l], conv_b[l], out[l], with_p6 ? p6 : nullptr,
-                          N, H[l], W[l], tw, 0, 0.01f, stream);
+                          N, H[l], W[l], tw, 0, 0.01f, fork.stream(l));
     if (rc != UFPN_OK) return rc;
   }
   return UFPN_OK;
@@ -857,20 +931,27 @@ int ufpn_neck_train_backward(int dtype, int N, const int* cin, const int* H, con
       return rc;
     dp[3] = dp5;
   }
-  for (int l = 0; l < 4; ++l) {  // every level's 3x3 backward: dM_l, dW3_l, db3_l
-    rc = conv3x3_backward(dtype, merged[l], nullptr, flipped[l], dp[l], dm[l], grad_conv_w[l],
-                          grad_conv_b[l], N, H[l], W[l], stream);
-    if (rc != UFPN_OK) return rc;
+  {  // every level's 3x3 backward (dM_l, dW3_l, db3_l): independent, on the level streams
+    LevelFork fork(s);
+    for (int l = 3; l >= 0; --l) {
+      rc = conv3x3_backward(dtype, merged[l], nullptr, flipped[l], dp[l], dm[l], grad_conv_w[l],
+                            grad_conv_b[l], N, H[l], W[l], fork.stream(l));
+      if (rc != UFPN_OK) return rc;
+    }
   }
   for (int l = 1; l < 4; ++l) {  // top-down adjoint, finest first: dM_l += up^T(dM_{l-1})
     rc = ufpn_upsample_add_backward(dtype, dm[l - 1], dm[l], dm[l], N, 256, H[l], W[l], H[l - 1],
                                     W[l - 1], stream);
     if (rc != UFPN_OK) return rc;
   }
-  for (int l = 0; l < 4; ++l) {  // laterals: dC_l, dWlat_l, dblat_l
-    rc = lateral_backward(dtype, x[l], nullptr, lat16_t[l], dm[l], grad_x ? grad_x[l] : nullptr,
-                          grad_lat_w[l], grad_lat_b[l], N, cin[l], H[l], W[l], stream);
-    if (rc != UFPN_OK) return rc;
+  {  // laterals (dC_l, dWlat_l, dblat_l): independent, on the level streams
+    LevelFork fork(s);
+    for (int l = 3; l >= 0; --l) {
+      rc = lateral_backward(dtype, x[l], nullptr, lat16_t[l], dm[l],
+                            grad_x ? grad_x[l] : nullptr, grad_lat_w[l], grad_lat_b[l], N, cin[l],
+                            H[l], W[l], fork.stream(l));
+      if (rc != UFPN_OK) return rc;
+    }
   }
   return UFPN_OK;
 }
