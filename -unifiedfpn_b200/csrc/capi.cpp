@@ -580,7 +580,7 @@ bool parse_16bit(int dtype, DType* dt) {
 // `main`.  One fork at a time per device (its lock is held until the join).
 struct SideStreams {
   cudaStream_t st[3] = {};
-  cudaEvent_t fork = nullptr;
+  cudaEvent_t fork = nullptr, step = nullptr;
   cudaEvent_t join[3] = {};
   bool ready = false;
   std::mutex mu;
@@ -601,6 +601,7 @@ SideStreams* side_streams() {
     for (auto& x : ss.st)
       ok = ok && cudaStreamCreateWithFlags(&x, cudaStreamNonBlocking) == cudaSuccess;
     ok = ok && cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming) == cudaSuccess;
+    ok = ok && cudaEventCreateWithFlags(&ss.step, cudaEventDisableTiming) == cudaSuccess;
     for (auto& e : ss.join)
       ok = ok && cudaEventCreateWithFlags(&e, cudaEventDisableTiming) == cudaSuccess;
     cudaThreadExchangeStreamCaptureMode(&mode);
@@ -632,6 +633,15 @@ class LevelFork {
   // level 0..3 = P2..P5
   void* stream(int level) const {
     return forked_ && level > 0 ? static_cast<void*>(ss_->st[level - 1]) : static_cast<void*>(main_);
+  }
+  // Makes `level`'s stream wait for the work issued on `from`'s stream so far (one event,
+  // re-recorded: a wait binds to the record before it, in eager mode and under capture alike).
+  cudaError_t order(int from, int level) const {
+    cudaStream_t a = static_cast<cudaStream_t>(stream(from));
+    cudaStream_t b = static_cast<cudaStream_t>(stream(level));
+    if (a == b) return cudaSuccess;
+    cudaError_t e = cudaEventRecord(ss_->step, a);
+    return e == cudaSuccess ? cudaStreamWaitEvent(b, ss_->step, 0) : e;
   }
 
  private:
@@ -857,16 +867,17 @@ int ufpn_neck_train_forward(int dtype, int N, const int* cin, const int* H, cons
   int rc = ufpn_prepare_neck_weights(dtype, 4, lat_w, cin, conv_w, lat16, lat16_t, packed,
                                      flipped, stream);
   if (rc != UFPN_OK) return rc;
-  for (int l = 3; l >= 0; --l) {  // top-down: M_l = lateral(C_l) + up(M_{l+1})
+  // Top-down on the caller's stream, M_l = lateral(C_l) + up(M_{l+1}); each level's 3x3 starts
+  // on its own stream as soon as M_l is written (P5, P4, P3 on side streams beside the next
+  // laterals, P2 on the caller's).
+  LevelFork fork(static_cast<cudaStream_t>(stream));
+  for (int l = 3; l >= 0; --l) {
     rc = ufpn_lateral_conv(dtype, UFPN_LAYOUT_NHWC, x[l], lat16[l], lat_b[l],
                            l < 3 ? merged[l + 1] : nullptr, merged[l], N, cin[l], H[l], W[l], 256,
                            l < 3 ? H[l + 1] : 0, l < 3 ? W[l + 1] : 0, stream);
     if (rc != UFPN_OK) return rc;
-  }
-  // The four 3x3s are independent: P5, P4, P3 on side streams, P2 on the caller's (the side
-  // levels enqueued first, so that their grids get SMs beside the P2 3x3's).
-  LevelFork fork(static_cast<cudaStream_t>(stream));
-  for (int l = 3; l >= 0; --l) {
+    cudaError_t e = fork.order(0, l);
+    if (e != cudaSuccess) return cuda_fail(e, "level fork");
     // 3x3s on single-CTA halo tiles, with the mixed tiling or the transposed view where that
     // needs fewer tiles (not with the fused P6): 2-5 % faster per training step than CTA pairs
     // on the own view
@@ -931,27 +942,28 @@ int ufpn_neck_train_backward(int dtype, int N, const int* cin, const int* H, con
       return rc;
     dp[3] = dp5;
   }
-  {  // every level's 3x3 backward (dM_l, dW3_l, db3_l): independent, on the level streams
-    LevelFork fork(s);
-    for (int l = 3; l >= 0; --l) {
-      rc = conv3x3_backward(dtype, merged[l], nullptr, flipped[l], dp[l], dm[l], grad_conv_w[l],
-                            grad_conv_b[l], N, H[l], W[l], fork.stream(l));
-      if (rc != UFPN_OK) return rc;
-    }
-  }
-  for (int l = 1; l < 4; ++l) {  // top-down adjoint, finest first: dM_l += up^T(dM_{l-1})
-    rc = ufpn_upsample_add_backward(dtype, dm[l - 1], dm[l], dm[l], N, 256, H[l], W[l], H[l - 1],
-                                    W[l - 1], stream);
+  // Level l's stream: its 3x3 backward (dM_l, dW3_l, db3_l), then, once dM_{l-1} is final, the
+  // top-down adjoint dM_l += up^T(dM_{l-1}), then its lateral backward (dC_l, dWlat_l, dblat_l).
+  // dM2 is final after its own 3x3 backward, so the P2 lateral runs on the caller's stream
+  // while the adjoint walks down P3..P5 on the side streams.
+  LevelFork fork(s);
+  for (int l = 3; l >= 0; --l) {
+    rc = conv3x3_backward(dtype, merged[l], nullptr, flipped[l], dp[l], dm[l], grad_conv_w[l],
+                          grad_conv_b[l], N, H[l], W[l], fork.stream(l));
     if (rc != UFPN_OK) return rc;
   }
-  {  // laterals (dC_l, dWlat_l, dblat_l): independent, on the level streams
-    LevelFork fork(s);
-    for (int l = 3; l >= 0; --l) {
-      rc = lateral_backward(dtype, x[l], nullptr, lat16_t[l], dm[l],
-                            grad_x ? grad_x[l] : nullptr, grad_lat_w[l], grad_lat_b[l], N, cin[l],
-                            H[l], W[l], fork.stream(l));
-      if (rc != UFPN_OK) return rc;
-    }
+  // (every adjoint is enqueued before any lateral, so that each wait covers the level above's
+  // 3x3 backward and adjoint and nothing after them)
+  for (int l = 1; l < 4; ++l) {
+    if ((e = fork.order(l - 1, l)) != cudaSuccess) return cuda_fail(e, "level fork");
+    rc = ufpn_upsample_add_backward(dtype, dm[l - 1], dm[l], dm[l], N, 256, H[l], W[l], H[l - 1],
+                                    W[l - 1], fork.stream(l));
+    if (rc != UFPN_OK) return rc;
+  }
+  for (int l = 3; l >= 0; --l) {
+    rc = lateral_backward(dtype, x[l], nullptr, lat16_t[l], dm[l], grad_x ? grad_x[l] : nullptr,
+                          grad_lat_w[l], grad_lat_b[l], N, cin[l], H[l], W[l], fork.stream(l));
+    if (rc != UFPN_OK) return rc;
   }
   return UFPN_OK;
 }
