@@ -570,18 +570,25 @@ bool parse_16bit(int dtype, DType* dt) {
   return parse_dtype(dtype, dt) && (*dt == DType::BF16 || *dt == DType::F16);
 }
 
-// Per-level work of a training step on up to four streams: a LevelFork makes three side
-// streams wait for everything enqueued on `main` so far, hands out a stream per level --
-// P5, P4, P3 on the side streams, P2 (the largest) on `main` -- and, when it goes out of
-// scope, makes `main` wait for the side streams.  The small levels' grids (20-70 CTAs) then
-// share the GPU with the large ones instead of holding it alone; a captured step becomes one
-// graph with the same fork and join.  The side streams and events are made once per device
-// (outside a capture: the first, eager step); if they cannot be made, every level runs on
-// `main`.  One fork at a time per device (its lock is held until the join).
+// Per-level work of a training step on several streams.  A StreamFork makes its side streams
+// wait for everything enqueued on `main` so far and, when it goes out of scope, makes `main`
+// wait for them; `order(a, b)` makes stream b wait for what was enqueued on stream a so far.
+//   * forward: one stream per level -- P5, P4, P3 on side streams, P2 (the largest) on `main`;
+//   * backward: per level a chain stream (the device's greatest priority) for the work on the
+//     critical path -- input gradients, the top-down adjoint, lateral input gradients -- and
+//     a weight-gradient stream (the least priority) for the weight and bias gradients, which
+//     nothing else reads: the chains' CTAs take SMs first as they free.
+// The small levels' grids (20-70 CTAs) then share the GPU with the large ones instead of
+// holding it alone; a captured step becomes one graph with the same fork and join.  The
+// streams and events are made once per device (outside a capture: the first, eager step); if
+// they cannot be made, everything runs on `main`.  One fork at a time per device (its lock is
+// held until the join).
 struct SideStreams {
-  cudaStream_t st[3] = {};
+  cudaStream_t fwd[3] = {};    // forward: P3..P5
+  cudaStream_t chain[4] = {};  // backward: P2..P5, greatest priority
+  cudaStream_t grads[4] = {};  // backward: P2..P5, least priority
   cudaEvent_t fork = nullptr, step = nullptr;
-  cudaEvent_t join[3] = {};
+  cudaEvent_t join[8] = {};
   bool ready = false;
   std::mutex mu;
 };
@@ -597,48 +604,60 @@ SideStreams* side_streams() {
     // process does not refuse the calls; the thread's own mode is restored after)
     cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
     cudaThreadExchangeStreamCaptureMode(&mode);
-    bool ok = true;
-    for (auto& x : ss.st)
+    int least = 0, greatest = 0;
+    bool ok = cudaDeviceGetStreamPriorityRange(&least, &greatest) == cudaSuccess;
+    for (auto& x : ss.fwd)
       ok = ok && cudaStreamCreateWithFlags(&x, cudaStreamNonBlocking) == cudaSuccess;
+    for (auto& x : ss.chain)
+      ok = ok && cudaStreamCreateWithPriority(&x, cudaStreamNonBlocking, greatest) == cudaSuccess;
+    for (auto& x : ss.grads)
+      ok = ok && cudaStreamCreateWithPriority(&x, cudaStreamNonBlocking, least) == cudaSuccess;
     ok = ok && cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming) == cudaSuccess;
     ok = ok && cudaEventCreateWithFlags(&ss.step, cudaEventDisableTiming) == cudaSuccess;
     for (auto& e : ss.join)
       ok = ok && cudaEventCreateWithFlags(&e, cudaEventDisableTiming) == cudaSuccess;
     cudaThreadExchangeStreamCaptureMode(&mode);
     if (!ok) {
-      cudaGetLastError();  // (leaves no sticky error; every level then runs on `main`)
+      cudaGetLastError();  // (leaves no sticky error; everything then runs on `main`)
       return nullptr;
     }
     ss.ready = true;
   }
   return &ss;
 }
-class LevelFork {
+class StreamFork {
  public:
-  explicit LevelFork(cudaStream_t main) : main_(main), ss_(side_streams()) {
-    if (ss_) {
-      lock_ = std::unique_lock<std::mutex>(ss_->mu);
-      forked_ = cudaEventRecord(ss_->fork, main_) == cudaSuccess;
-      for (int i = 0; forked_ && i < 3; ++i)
-        forked_ = cudaStreamWaitEvent(ss_->st[i], ss_->fork, 0) == cudaSuccess;
+  StreamFork(cudaStream_t main, bool backward) : main_(main), ss_(side_streams()) {
+    if (!ss_) return;
+    lock_ = std::unique_lock<std::mutex>(ss_->mu);
+    if (backward) {
+      for (int l = 0; l < 4; ++l) side_[n_++] = ss_->chain[l];
+      for (int l = 0; l < 4; ++l) side_[n_++] = ss_->grads[l];
+    } else {
+      for (int l = 0; l < 3; ++l) side_[n_++] = ss_->fwd[l];
     }
+    forked_ = cudaEventRecord(ss_->fork, main_) == cudaSuccess;
+    for (int i = 0; forked_ && i < n_; ++i)
+      forked_ = cudaStreamWaitEvent(side_[i], ss_->fork, 0) == cudaSuccess;
+    backward_ = backward;
   }
-  ~LevelFork() {
+  ~StreamFork() {
     if (!forked_) return;
-    for (int i = 0; i < 3; ++i) {
-      cudaEventRecord(ss_->join[i], ss_->st[i]);
+    for (int i = 0; i < n_; ++i) {
+      cudaEventRecord(ss_->join[i], side_[i]);
       cudaStreamWaitEvent(main_, ss_->join[i], 0);
     }
   }
-  // level 0..3 = P2..P5
-  void* stream(int level) const {
-    return forked_ && level > 0 ? static_cast<void*>(ss_->st[level - 1]) : static_cast<void*>(main_);
+  // level 0..3 = P2..P5: the forward's level streams, or the backward's chain streams
+  cudaStream_t level(int l) const {
+    if (!forked_) return main_;
+    return backward_ ? ss_->chain[l] : l > 0 ? ss_->fwd[l - 1] : main_;
   }
-  // Makes `level`'s stream wait for the work issued on `from`'s stream so far (one event,
-  // re-recorded: a wait binds to the record before it, in eager mode and under capture alike).
-  cudaError_t order(int from, int level) const {
-    cudaStream_t a = static_cast<cudaStream_t>(stream(from));
-    cudaStream_t b = static_cast<cudaStream_t>(stream(level));
+  // the backward's weight-gradient streams
+  cudaStream_t grads(int l) const { return forked_ && backward_ ? ss_->grads[l] : main_; }
+  // Makes stream b wait for the work enqueued on stream a so far (one event, re-recorded: a
+  // wait binds to the record before it, in eager mode and under capture alike).
+  cudaError_t order(cudaStream_t a, cudaStream_t b) const {
     if (a == b) return cudaSuccess;
     cudaError_t e = cudaEventRecord(ss_->step, a);
     return e == cudaSuccess ? cudaStreamWaitEvent(b, ss_->step, 0) : e;
@@ -648,7 +667,9 @@ class LevelFork {
   cudaStream_t main_;
   SideStreams* ss_;
   std::unique_lock<std::mutex> lock_;
-  bool forked_ = false;
+  cudaStream_t side_[8] = {};
+  int n_ = 0;
+  bool forked_ = false, backward_ = false;
 };
 }  // namespace
 
@@ -870,13 +891,13 @@ int ufpn_neck_train_forward(int dtype, int N, const int* cin, const int* H, cons
   // Top-down on the caller's stream, M_l = lateral(C_l) + up(M_{l+1}); each level's 3x3 starts
   // on its own stream as soon as M_l is written (P5, P4, P3 on side streams beside the next
   // laterals, P2 on the caller's).
-  LevelFork fork(static_cast<cudaStream_t>(stream));
+  StreamFork fork(static_cast<cudaStream_t>(stream), false);
   for (int l = 3; l >= 0; --l) {
     rc = ufpn_lateral_conv(dtype, UFPN_LAYOUT_NHWC, x[l], lat16[l], lat_b[l],
                            l < 3 ? merged[l + 1] : nullptr, merged[l], N, cin[l], H[l], W[l], 256,
                            l < 3 ? H[l + 1] : 0, l < 3 ? W[l + 1] : 0, stream);
     if (rc != UFPN_OK) return rc;
-    cudaError_t e = fork.order(0, l);
+    cudaError_t e = fork.order(static_cast<cudaStream_t>(stream), fork.level(l));
     if (e != cudaSuccess) return cuda_fail(e, "level fork");
     // 3x3s on single-CTA halo tiles, with the mixed tiling or the transposed view where that
     // needs fewer tiles (not with the fused P6): 2-5 % faster per training step than CTA pairs
@@ -887,7 +908,7 @@ int ufpn_neck_train_forward(int dtype, int N, const int* cin, const int* H, cons
                    : ufpn::halo_transpose_pays(H[l], W[l])          ? -2
                                                                     : 0;
     rc = ufpn_conv3x3_act(dtype, merged[l], packed[l], conv_b[l], out[l], with_p6 ? p6 : nullptr,
-                          N, H[l], W[l], tw, 0, 0.01f, fork.stream(l));
+                          N, H[l], W[l], tw, 0, 0.01f, fork.level(l));
     if (rc != UFPN_OK) return rc;
   }
   return UFPN_OK;
@@ -942,28 +963,38 @@ int ufpn_neck_train_backward(int dtype, int N, const int* cin, const int* H, con
       return rc;
     dp[3] = dp5;
   }
-  // Level l's stream: its 3x3 backward (dM_l, dW3_l, db3_l), then, once dM_{l-1} is final, the
-  // top-down adjoint dM_l += up^T(dM_{l-1}), then its lateral backward (dC_l, dWlat_l, dblat_l).
-  // dM2 is final after its own 3x3 backward, so the P2 lateral runs on the caller's stream
-  // while the adjoint walks down P3..P5 on the side streams.
-  LevelFork fork(s);
+  // Level l's chain stream: the 3x3 input gradient dM_l, then -- once the level below's dM
+  // is final -- the top-down adjoint dM_l += up^T(dM_{l-1}), then the lateral input gradient
+  // dC_l.  Level l's weight-gradient stream: the 3x3's weight and bias gradients (from the
+  // start), then the lateral's once dM_l is final.  Every adjoint is enqueued before any
+  // lateral, so that each wait covers exactly the input gradient and adjoint before it.
+  StreamFork fork(s, true);
   for (int l = 3; l >= 0; --l) {
-    rc = conv3x3_backward(dtype, merged[l], nullptr, flipped[l], dp[l], dm[l], grad_conv_w[l],
-                          grad_conv_b[l], N, H[l], W[l], fork.stream(l));
+    rc = conv3x3_backward(dtype, nullptr, nullptr, flipped[l], dp[l], dm[l], nullptr, nullptr, N,
+                          H[l], W[l], fork.level(l));
+    if (rc != UFPN_OK) return rc;
+    rc = conv3x3_backward(dtype, merged[l], nullptr, nullptr, dp[l], nullptr, grad_conv_w[l],
+                          grad_conv_b[l], N, H[l], W[l], fork.grads(l));
     if (rc != UFPN_OK) return rc;
   }
-  // (every adjoint is enqueued before any lateral, so that each wait covers the level above's
-  // 3x3 backward and adjoint and nothing after them)
   for (int l = 1; l < 4; ++l) {
-    if ((e = fork.order(l - 1, l)) != cudaSuccess) return cuda_fail(e, "level fork");
+    if ((e = fork.order(fork.level(l - 1), fork.level(l))) != cudaSuccess)
+      return cuda_fail(e, "level fork");
     rc = ufpn_upsample_add_backward(dtype, dm[l - 1], dm[l], dm[l], N, 256, H[l], W[l], H[l - 1],
-                                    W[l - 1], fork.stream(l));
+                                    W[l - 1], fork.level(l));
     if (rc != UFPN_OK) return rc;
   }
   for (int l = 3; l >= 0; --l) {
-    rc = lateral_backward(dtype, x[l], nullptr, lat16_t[l], dm[l], grad_x ? grad_x[l] : nullptr,
-                          grad_lat_w[l], grad_lat_b[l], N, cin[l], H[l], W[l], fork.stream(l));
+    if ((e = fork.order(fork.level(l), fork.grads(l))) != cudaSuccess)
+      return cuda_fail(e, "level fork");
+    rc = lateral_backward(dtype, x[l], nullptr, nullptr, dm[l], nullptr, grad_lat_w[l],
+                          grad_lat_b[l], N, cin[l], H[l], W[l], fork.grads(l));
     if (rc != UFPN_OK) return rc;
+    if (grad_x) {
+      rc = lateral_backward(dtype, nullptr, nullptr, lat16_t[l], dm[l], grad_x[l], nullptr,
+                            nullptr, N, cin[l], H[l], W[l], fork.level(l));
+      if (rc != UFPN_OK) return rc;
+    }
   }
   return UFPN_OK;
 }

@@ -113,12 +113,9 @@ SIGNATURES = {
     "ufpn_prepare_neck_weights": (
         c_int, [c_int, c_int, POINTER(c_void_p), POINTER(c_int), POINTER(c_void_p), POINTER(c_void_p),
                 POINTER(c_void_p), POINTER(c_void_p), POINTER(c_void_p), c_void_p]),
-    "ufpn_neck_train_forward": (
-        c_int, [c_int, c_int, POINTER(c_int), POINTER(c_int), POINTER(c_int)] + [POINTER(c_void_p)] * 11
-        + [c_void_p, c_void_p]),
-    "ufpn_neck_train_backward": (
-        c_int, [c_int, c_int, POINTER(c_int), POINTER(c_int), POINTER(c_int)] + [POINTER(c_void_p)] * 5
-        + [c_void_p] + [POINTER(c_void_p)] * 5 + [c_void_p]),
+    # (the array arguments of the two training drivers are passed as addresses)
+    "ufpn_neck_train_forward": (c_int, [c_int, c_int] + [c_void_p] * 16),
+    "ufpn_neck_train_backward": (c_int, [c_int, c_int] + [c_void_p] * 15),
     "ufpn_upsample_add_backward": (
         c_int, [c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p]),
     "ufpn_p6_backward": (c_int, [c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p]),

@@ -18,6 +18,7 @@ allocates the results.  ``FPNNeck`` wraps both in a ``torch.nn.Module`` with fp3
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Sequence
 
 import torch
@@ -29,59 +30,93 @@ from .ops import _DT
 _CL = torch.channels_last
 
 
-def _ptrs(ts):
-    return (_lib.c_void_p * len(ts))(*[t.data_ptr() if t is not None else None for t in ts])
+def _f32(t: torch.Tensor, dev: torch.device) -> torch.Tensor:
+    """``t`` as fp32, contiguous on ``dev`` (``t`` itself when it already is)."""
+    if t.dtype is torch.float32 and t.is_contiguous() and t.device == dev:
+        return t
+    return t.detach().to(device=dev, dtype=torch.float32).contiguous()
 
 
-def _ints(vs):
-    return (_lib.c_int * len(vs))(*vs)
+def _layout(t: torch.Tensor, dt: torch.dtype, dev: torch.device) -> torch.Tensor:
+    """``t`` in ``dt``, channels_last on ``dev`` (``t`` itself when it already is)."""
+    if t.dtype is dt and t.is_contiguous(memory_format=_CL) and t.device == dev:
+        return t
+    return t.to(device=dev, dtype=dt).contiguous(memory_format=_CL)
+
+
+def _arrays(ints, ptrs):
+    """The driver calls' array arguments as two ctypes arrays (kept alive by the caller) and
+    the address of each: ``int_at(k)`` / ``ptr_at(k)`` = address of element k."""
+    ia = (ctypes.c_int * len(ints))(*ints)
+    pa = (ctypes.c_void_p * len(ptrs))(*ptrs)
+    ib, pb = ctypes.addressof(ia), ctypes.addressof(pa)
+    return ia, pa, (lambda k: ib + 4 * k), (lambda k: pb + 8 * k)
+
+
+def _workspace_layout(N, cin, H, W, esz):
+    """Byte offsets (256-byte aligned) of the forward's saved intermediates in one buffer: per
+    level the 16-bit lateral weights [256][Cin], their transpose [ceil(Cin/256)*256][256], the
+    packed and the flipped 3x3 weights [256][9][256], then the merged maps M2..M5 (NHWC)."""
+    sizes = []
+    for c in cin:
+        sizes += [256 * c, (c + 255) // 256 * 256 * 256, 256 * 9 * 256, 256 * 9 * 256]
+    sizes += [N * h * w * 256 for h, w in zip(H, W)]
+    offs, total = [], 0
+    for n in sizes:
+        offs.append(total)
+        total += (n * esz + 255) // 256 * 256
+    return offs, total
 
 
 def fpn_neck_forward_train(feats: Sequence[torch.Tensor], lateral_w: Sequence[torch.Tensor],
                            lateral_b: Sequence[torch.Tensor], output_w: Sequence[torch.Tensor],
                            output_b: Sequence[torch.Tensor], return_p6: bool = True):
     """Forward of the neck for training.  ``feats``: C2..C5 (bf16 / fp16, 4-D CUDA); weights
-    as for ``UnifiedFPN.initialize_weights`` (lateral [256, Cin], 3x3 [256, 256, 3, 3], fp32
-    biases).  Returns ``(outputs, saved)``: P2..P5 (and P6) channels_last, and the state
-    ``fpn_neck_backward`` needs (the inputs, the merged maps M2..M5, the prepared weights).
-    One library call (``ufpn_neck_train_forward``): the weight layouts of the whole step in
-    one launch, the four laterals top-down, the four 3x3s (CTA-pair halo tiles)."""
+    as for ``UnifiedFPN.initialize_weights`` (lateral [256, Cin] or [256, Cin, 1, 1], 3x3
+    [256, 256, 3, 3], fp32 biases).  Returns ``(outputs, saved)``: P2..P5 (and P6)
+    channels_last, and the opaque state ``fpn_neck_backward`` needs (the inputs, and one
+    workspace holding the merged maps M2..M5 and the prepared weight layouts).  One library
+    call (``ufpn_neck_train_forward``): the weight layouts of the whole step in one launch, the
+    four laterals top-down, the four 3x3s (single-CTA halo tiles)."""
     if len(feats) != 4 or len(lateral_w) != 4 or len(output_w) != 4:
         raise ValueError("feats and weights must be C2..C5 / four levels")
     dt = feats[0].dtype
-    if dt not in (torch.bfloat16, torch.float16) or any(f.dtype != dt for f in feats):
+    if dt not in (torch.bfloat16, torch.float16) or any(f.dtype is not dt for f in feats):
         raise ValueError("training runs on bf16 or fp16 features of one dtype")
-    if any(not f.is_cuda for f in feats) or feats[0].dim() != 4:
+    if any(not f.is_cuda or f.dim() != 4 for f in feats):
         raise ValueError("features must be 4-D CUDA tensors")
     dev = feats[0].device
-    x = [f.contiguous(memory_format=_CL) for f in feats]
+    x = [f if f.is_contiguous(memory_format=_CL) else f.contiguous(memory_format=_CL) for f in feats]
     N = x[0].shape[0]
     cin = [f.shape[1] for f in x]
     H = [f.shape[2] for f in x]
     W = [f.shape[3] for f in x]
-    lat32 = [w.detach().reshape(256, -1).to(device=dev, dtype=torch.float32).contiguous() for w in lateral_w]
-    conv32 = [w.detach().to(device=dev, dtype=torch.float32).contiguous() for w in output_w]
-    latb = [b.detach().to(device=dev, dtype=torch.float32).contiguous() for b in lateral_b]
-    convb = [b.detach().to(device=dev, dtype=torch.float32).contiguous() for b in output_b]
-    if any(w.shape[1] != c for w, c in zip(lat32, cin)) or any(tuple(w.shape) != (256, 256, 3, 3) for w in conv32):
+    lat32 = [_f32(w, dev) for w in lateral_w]
+    conv32 = [_f32(w, dev) for w in output_w]
+    latb = [_f32(b, dev) for b in lateral_b]
+    convb = [_f32(b, dev) for b in output_b]
+    if any(w.shape[0] != 256 or w.numel() != 256 * c for w, c in zip(lat32, cin)) or any(
+            w.shape != (256, 256, 3, 3) for w in conv32):
         raise ValueError("lateral weights must be [256, Cin] and 3x3 weights [256, 256, 3, 3]")
-    lw = [torch.empty(256, c, device=dev, dtype=dt) for c in cin]
-    lw_t = [torch.empty((c + 255) // 256 * 256, 256, device=dev, dtype=dt) for c in cin]
-    packed = [torch.empty(256, 9, 256, device=dev, dtype=dt) for _ in cin]
-    flipped = [torch.empty(256, 9, 256, device=dev, dtype=dt) for _ in cin]
-    merged = [torch.empty(N, 256, h, w, device=dev, dtype=dt, memory_format=_CL) for h, w in zip(H, W)]
+    offs, total = _workspace_layout(N, cin, H, W, 2)
+    ws = torch.empty(total, device=dev, dtype=torch.uint8)
+    base = ws.data_ptr()
     outs = [torch.empty(N, 256, h, w, device=dev, dtype=dt, memory_format=_CL) for h, w in zip(H, W)]
     p6 = torch.empty(N, 256, (H[3] - 1) // 2 + 1, (W[3] - 1) // 2 + 1, device=dev, dtype=dt,
                      memory_format=_CL) if return_p6 else None
-    check(lib.ufpn_neck_train_forward(_DT[dt], N, _ints(cin), _ints(H), _ints(W), _ptrs(x), _ptrs(lat32),
-                                      _ptrs(latb), _ptrs(conv32), _ptrs(convb), _ptrs(lw), _ptrs(lw_t),
-                                      _ptrs(packed), _ptrs(flipped), _ptrs(merged), _ptrs(outs),
+    lay = [[base + offs[4 * l + k] for l in range(4)] for k in range(4)]  # lw, lw_t, packed, flipped
+    merged = [base + offs[16 + l] for l in range(4)]
+    ptrs = ([t.data_ptr() for t in x] + [t.data_ptr() for t in lat32] + [t.data_ptr() for t in latb]
+            + [t.data_ptr() for t in conv32] + [t.data_ptr() for t in convb] + lay[0] + lay[1]
+            + lay[2] + lay[3] + merged + [t.data_ptr() for t in outs])
+    ia, pa, ip, pp = _arrays(cin + H + W, ptrs)
+    check(lib.ufpn_neck_train_forward(_DT[dt], N, ip(0), ip(4), ip(8), *[pp(4 * k) for k in range(11)],
                                       p6.data_ptr() if p6 is not None else None,
                                       torch.cuda.current_stream(dev).cuda_stream), "ufpn_neck_train_forward")
     if return_p6:
         outs.append(p6)
-    return outs, {"x": x, "merged": merged, "lateral_w": lw, "lateral_w_t": lw_t, "packed": packed,
-                  "flipped": flipped}
+    return outs, {"x": x, "workspace": ws, "merged": merged, "lateral_w_t": lay[1],
+                  "flipped": lay[3], "sizes": (N, cin, H, W)}
 
 
 def fpn_neck_backward(grad_outputs: Sequence[torch.Tensor | None], saved: dict,
@@ -89,37 +124,39 @@ def fpn_neck_backward(grad_outputs: Sequence[torch.Tensor | None], saved: dict,
     """Gradients of the neck given dP2..dP5 (and dP6; None = zero) and ``saved`` from
     ``fpn_neck_forward_train``.  Returns a dict: ``grad_inputs`` (dC2..dC5, or None),
     ``grad_lateral_w`` ([256, Cin] fp32), ``grad_lateral_b``, ``grad_output_w``
-    ([256, 256, 3, 3] fp32), ``grad_output_b``.  One library call
-    (``ufpn_neck_train_backward``)."""
-    x, merged, lw_t, flipped = saved["x"], saved["merged"], saved["lateral_w_t"], saved["flipped"]
+    ([256, 256, 3, 3] fp32), ``grad_output_b``; the fp32 gradients are views of one buffer.
+    One library call (``ufpn_neck_train_backward``)."""
+    x = saved["x"]
+    N, cin, H, W = saved["sizes"]
     dt = x[0].dtype
     dev = x[0].device
-    N = x[0].shape[0]
-    cin = [f.shape[1] for f in x]
-    H = [f.shape[2] for f in x]
-    W = [f.shape[3] for f in x]
 
-    def g16(g, shape):
+    def g16(l, shape):
+        g = grad_outputs[l] if l < len(grad_outputs) else None
         if g is None:
             return None
-        if tuple(g.shape) != shape:
+        if g.shape != shape:
             raise ValueError(f"output gradient of shape {tuple(g.shape)}, expected {shape}")
-        return g.to(device=dev, dtype=dt).contiguous(memory_format=_CL)
+        return _layout(g, dt, dev)
 
-    dp = [g16(grad_outputs[l] if l < len(grad_outputs) else None, (N, 256, H[l], W[l])) for l in range(4)]
-    g6 = None
-    if len(grad_outputs) > 4 and grad_outputs[4] is not None:
-        g6 = g16(grad_outputs[4], (N, 256, (H[3] - 1) // 2 + 1, (W[3] - 1) // 2 + 1))
+    dp = [g16(l, (N, 256, H[l], W[l])) for l in range(4)]
+    g6 = g16(4, (N, 256, (H[3] - 1) // 2 + 1, (W[3] - 1) // 2 + 1))
     gx = [torch.empty_like(f, memory_format=_CL) for f in x] if need_input_grad else None
-    gwl = [torch.empty(256, c, device=dev, dtype=torch.float32) for c in cin]
-    gbl = [torch.empty(256, device=dev, dtype=torch.float32) for _ in cin]
-    gw3 = [torch.empty(256, 256, 3, 3, device=dev, dtype=torch.float32) for _ in cin]
-    gb3 = [torch.empty(256, device=dev, dtype=torch.float32) for _ in cin]
-    check(lib.ufpn_neck_train_backward(_DT[dt], N, _ints(cin), _ints(H), _ints(W), _ptrs(x), _ptrs(merged),
-                                       _ptrs(lw_t), _ptrs(flipped), _ptrs(dp),
-                                       g6.data_ptr() if g6 is not None else None,
-                                       _ptrs(gx) if gx is not None else None, _ptrs(gwl), _ptrs(gbl),
-                                       _ptrs(gw3), _ptrs(gb3), torch.cuda.current_stream(dev).cuda_stream),
+    sizes = [256 * c for c in cin] + [256] * 4 + [256 * 2304] * 4 + [256] * 4
+    parts = torch.empty(sum(sizes), device=dev, dtype=torch.float32).split(sizes)
+    gwl = [parts[l].view(256, c) for l, c in enumerate(cin)]
+    gbl = list(parts[4:8])
+    gw3 = [parts[8 + l].view(256, 256, 3, 3) for l in range(4)]
+    gb3 = list(parts[12:16])
+    ptrs = ([t.data_ptr() for t in x] + saved["merged"] + saved["lateral_w_t"]
+            + saved["flipped"] + [g.data_ptr() if g is not None else None for g in dp]
+            + ([t.data_ptr() for t in gx] if gx is not None else [None] * 4)
+            + [t.data_ptr() for t in parts])
+    ia, pa, ip, pp = _arrays(cin + H + W, ptrs)
+    check(lib.ufpn_neck_train_backward(_DT[dt], N, ip(0), ip(4), ip(8), pp(0), pp(4), pp(8), pp(12),
+                                       pp(16), g6.data_ptr() if g6 is not None else None,
+                                       pp(20) if gx is not None else None, pp(24), pp(28), pp(32),
+                                       pp(36), torch.cuda.current_stream(dev).cuda_stream),
           "ufpn_neck_train_backward")
     return {"grad_inputs": gx, "grad_lateral_w": gwl, "grad_lateral_b": gbl, "grad_output_w": gw3,
             "grad_output_b": gb3}
@@ -132,7 +169,7 @@ class _NeckFunction(torch.autograd.Function):
         outs, saved = fpn_neck_forward_train([c2, c3, c4, c5], lw, lb, ow, ob, return_p6)
         ctx.saved = saved
         ctx.weight_dtypes = [p.dtype for p in params]
-        ctx.lateral_shapes = [tuple(w.shape) for w in lw]
+        ctx.lateral_shapes = [w.shape for w in lw]
         ctx.input_dtypes = [c.dtype for c in (c2, c3, c4, c5)]
         ctx.return_p6 = return_p6
         return tuple(outs)
@@ -140,15 +177,20 @@ class _NeckFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, *grads):
         need_x = any(ctx.needs_input_grad[1:5])
-        r = fpn_neck_backward(list(grads), ctx.saved, need_input_grad=need_x)
+        r = fpn_neck_backward(grads, ctx.saved, need_input_grad=need_x)
+        ctx.saved = None
         gx = r["grad_inputs"] if need_x else [None] * 4
         wd = ctx.weight_dtypes
-        gl = [g.reshape(s).to(wd[i]) for i, (g, s) in enumerate(zip(r["grad_lateral_w"], ctx.lateral_shapes))]
-        gbl = [g.to(wd[4 + i]) for i, g in enumerate(r["grad_lateral_b"])]
-        gw3 = [g.to(wd[8 + i]) for i, g in enumerate(r["grad_output_w"])]
-        gb3 = [g.to(wd[12 + i]) for i, g in enumerate(r["grad_output_b"])]
-        ctx.saved = None
-        return (None, *[g.to(d) if g is not None else None for g, d in zip(gx, ctx.input_dtypes)],
+
+        def cast(g, d, shape=None):
+            if shape is not None and g.shape != shape:
+                g = g.reshape(shape)
+            return g if g.dtype is d else g.to(d)
+        gl = [cast(g, wd[i], s) for i, (g, s) in enumerate(zip(r["grad_lateral_w"], ctx.lateral_shapes))]
+        gbl = [cast(g, wd[4 + i]) for i, g in enumerate(r["grad_lateral_b"])]
+        gw3 = [cast(g, wd[8 + i]) for i, g in enumerate(r["grad_output_w"])]
+        gb3 = [cast(g, wd[12 + i]) for i, g in enumerate(r["grad_output_b"])]
+        return (None, *[cast(g, d) if g is not None else None for g, d in zip(gx, ctx.input_dtypes)],
                 *gl, *gbl, *gw3, *gb3)
 
 
@@ -174,7 +216,10 @@ class FPNNeck(torch.nn.Module):
         self.output_b = torch.nn.ParameterList([torch.nn.Parameter(torch.zeros(256)) for _ in in_channels])
 
     def forward(self, feats: Sequence[torch.Tensor]):
-        params = [*self.lateral_w, *self.lateral_b, *self.output_w, *self.output_b]
+        # (the lists' registered parameters in index order, without ParameterList's per-item
+        # lookups)
+        params = [*self.lateral_w._parameters.values(), *self.lateral_b._parameters.values(),
+                  *self.output_w._parameters.values(), *self.output_b._parameters.values()]
         return list(_NeckFunction.apply(self.return_p6, *feats, *params))
 
     def make_graphed(self, sample_feats: Sequence[torch.Tensor]):
