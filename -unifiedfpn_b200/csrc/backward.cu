@@ -16,7 +16,7 @@
 //     are contiguous, i.e. MN-major operands, read through MN-major 128-byte-swizzle
 //     descriptors; the 3x3 taps shift the X box (TMA zero-fills outside the image = pad 1).
 //     The pixel range is split over CTAs (split-K); each CTA writes its fp32 partial and
-//     reduce_partials_kernel adds the partials in a fixed order.
+//     reduce_partials_kernel / reduce_partials_taps9_kernel add the partials in a fixed order.
 //   * bias gradients: column sums of dY in fp32, per block then in a fixed order.
 //   * input gradients reuse the forward kernels: the 1x1 lateral with the transposed weights
 //     (one 256-channel slice of dX per launch) and the 3x3 with the weights transposed in
@@ -329,40 +329,80 @@ __device__ __forceinline__ float fixed_order_sum(int n, F v) {
   return (a0 + a1) + (a2 + a3);
 }
 
-// out[(o * Cin + c) * taps + t] = sum over s of partial[s][t][o][c] (for the 3x3 the
-// [256][256][3][3] order of its fp32 weights), in a fixed order: four
-// running sums over s = 0, 4, 8, .. / 1, 5, 9, .. / .., added last (four loads in flight per
-// thread instead of one dependent chain of ksplit loads)
-// (With grad_b: indices per .. per + 255 sum the db_rows rows db_partial[r][o] the same way
-// into grad_b[o].)
+// The same fixed order per element for a 16-byte vector of four outputs, spread over a group
+// of four lanes: lane k sums the vectors s = k, k + 4, k + 8, .. in order (four loads in
+// flight), then the group adds its chains as (c0 + c1) + (c2 + c3) -- fixed_order_sum's
+// association, so every element comes out bitwise as from fixed_order_sum -- and lane 0 of
+// the group holds the result.  All four lanes of a group must call it.
+__device__ __forceinline__ float4 fixed_order_sum4(const float* p, long long stride, int n) {
+  const int k = static_cast<int>(threadIdx.x) & 3;
+  float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+  auto add = [&](const float4 t) {
+    a.x += t.x;
+    a.y += t.y;
+    a.z += t.z;
+    a.w += t.w;
+  };
+  int s = k;
+  for (; s + 12 < n; s += 16) {
+    const float4 t0 = __ldg(reinterpret_cast<const float4*>(p + s * stride));
+    const float4 t1 = __ldg(reinterpret_cast<const float4*>(p + (s + 4) * stride));
+    const float4 t2 = __ldg(reinterpret_cast<const float4*>(p + (s + 8) * stride));
+    const float4 t3 = __ldg(reinterpret_cast<const float4*>(p + (s + 12) * stride));
+    add(t0);
+    add(t1);
+    add(t2);
+    add(t3);
+  }
+  for (; s < n; s += 4) add(__ldg(reinterpret_cast<const float4*>(p + s * stride)));
+  float4 b;
+  b.x = __shfl_xor_sync(0xffffffffu, a.x, 1);
+  b.y = __shfl_xor_sync(0xffffffffu, a.y, 1);
+  b.z = __shfl_xor_sync(0xffffffffu, a.z, 1);
+  b.w = __shfl_xor_sync(0xffffffffu, a.w, 1);
+  a.x += b.x;  // lane 0: c0 + c1, lane 2: c2 + c3
+  a.y += b.y;
+  a.z += b.z;
+  a.w += b.w;
+  b.x = __shfl_xor_sync(0xffffffffu, a.x, 2);
+  b.y = __shfl_xor_sync(0xffffffffu, a.y, 2);
+  b.z = __shfl_xor_sync(0xffffffffu, a.z, 2);
+  b.w = __shfl_xor_sync(0xffffffffu, a.w, 2);
+  return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+}
+
+// 1x1 weight gradient: out[o * Cin + c] = sum over s of partial[s][o][c] in the fixed order,
+// four lanes per 16-byte vector of outputs (Cin a multiple of 4).  With grad_b, the block
+// after the last one sums the db_rows rows db_partial[r][o] the same way into grad_b[o].
 __global__ void __launch_bounds__(256) reduce_partials_kernel(const float* __restrict__ partial,
                                                               float* __restrict__ out, int ksplit,
-                                                              int taps, int Cin,
+                                                              int Cin,
                                                               const float* __restrict__ db_partial,
                                                               float* __restrict__ grad_b,
                                                               int db_rows) {
-  const long long per = static_cast<long long>(taps) * 256 * Cin;
-  const long long total = per + (grad_b ? 256 : 0);
-  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    if (i >= per) {
-      const int o = static_cast<int>(i - per);
-      grad_b[o] = fixed_order_sum(db_rows, [&](int r) { return __ldg(db_partial + r * 256 + o); });
-      continue;
-    }
-    const float acc = fixed_order_sum(ksplit, [&](int sp) { return __ldg(partial + sp * per + i); });
-    const int c = static_cast<int>(i % Cin);
-    const long long to = i / Cin;
-    const int o = static_cast<int>(to % 256);
-    const int t = static_cast<int>(to / 256);
-    out[(static_cast<size_t>(o) * Cin + c) * taps + t] = acc;  // [o][c][ky][kx] (taps 9)
+  const long long per = 256LL * Cin;
+  const long long vblocks = (per / 4 + 63) / 64;
+  if (static_cast<long long>(blockIdx.x) >= vblocks) {  // bias
+    const int o = threadIdx.x;
+    grad_b[o] = fixed_order_sum(db_rows, [&](int r) { return __ldg(db_partial + r * 256 + o); });
+    return;
+  }
+  // (every lane takes part in the group's shuffles; a lane past the end sums nothing)
+  const long long v = static_cast<long long>(blockIdx.x) * 64 + threadIdx.x / 4;
+  const bool in = v * 4 < per;
+  const float4 r = fixed_order_sum4(partial + (in ? v * 4 : 0), per, in ? ksplit : 0);
+  if (in && (threadIdx.x & 3) == 0) {  // (scalar stores: grad_w need only be 4-byte aligned)
+    out[v * 4 + 0] = r.x;
+    out[v * 4 + 1] = r.y;
+    out[v * 4 + 2] = r.z;
+    out[v * 4 + 3] = r.w;
   }
 }
 
-// 3x3 weight gradient in [256 o][Cin c][9 t] order: block (o, c0) sums partial[s][t][o][c0 + cc]
-// for its 9 x 32 outputs (thread (t, cc): coalesced 128-byte reads per t), stages them as
-// [cc][t] and writes the 288 contiguous outputs in order.  The last block (with grad_b) sums
-// the bias partials.  Same fixed order as reduce_partials_kernel.
+// 3x3 weight gradient in [256 o][Cin c][9 t] order: block (o, c0) sums partial[s][t][o][c0 ..
+// c0 + 31] for its 9 x 32 outputs -- thread (t, vector, lane): four lanes per 16-byte vector,
+// fixed_order_sum4 -- stages them as [cc][t] and writes the 288 contiguous outputs in order.
+// The last block (with grad_b) sums the bias partials.  Cin a multiple of 4.
 __global__ void __launch_bounds__(288) reduce_partials_taps9_kernel(
     const float* __restrict__ partial, float* __restrict__ out, int ksplit, int Cin,
     const float* __restrict__ db_partial, float* __restrict__ grad_b, int db_rows) {
@@ -376,11 +416,20 @@ __global__ void __launch_bounds__(288) reduce_partials_taps9_kernel(
   }
   const int o = static_cast<int>(blockIdx.x) / cblocks;
   const int c0 = (static_cast<int>(blockIdx.x) % cblocks) * 32;
-  const int t = threadIdx.x / 32, cc = threadIdx.x % 32;
+  const int t = threadIdx.x / 32, cv = (threadIdx.x % 32) / 4;
   const long long per = 9LL * 256 * Cin;
-  const size_t idx = (static_cast<size_t>(t) * 256 + o) * Cin + c0 + cc;
-  if (c0 + cc < Cin)
-    tile[cc * 9 + t] = fixed_order_sum(ksplit, [&](int s) { return __ldg(partial + s * per + idx); });
+  // (every lane takes part in the group's shuffles; a vector past Cin sums nothing)
+  const bool in = c0 + cv * 4 < Cin;
+  const size_t idx = in ? (static_cast<size_t>(t) * 256 + o) * Cin + c0 + cv * 4 : 0;
+  const float4 r = fixed_order_sum4(partial + idx, per, in ? ksplit : 0);
+  {
+    if (in && (threadIdx.x & 3) == 0) {
+      tile[(cv * 4 + 0) * 9 + t] = r.x;
+      tile[(cv * 4 + 1) * 9 + t] = r.y;
+      tile[(cv * 4 + 2) * 9 + t] = r.z;
+      tile[(cv * 4 + 3) * 9 + t] = r.w;
+    }
+  }
   __syncthreads();
   const int j = threadIdx.x;  // output element c0 * 9 + j of row o
   if (c0 + j / 9 < Cin) out[(static_cast<size_t>(o) * Cin + c0) * 9 + j] = tile[j];
@@ -828,15 +877,17 @@ struct PrepArgs {
   void* out[kPrepMaxJobs];
   int kind[kPrepMaxJobs];
   int cin[kPrepMaxJobs];
+  int vec[kPrepMaxJobs];  // kinds 0 / 1: in (and for kind 0 out) 16-byte aligned
   int num_jobs;
 };
 
 // One block per unit of a job (WeightPrepJob kinds), 256 threads; every thread reads adjacent
 // fp32 words and every warp writes consecutive elements.
-//   kind 0: unit = output row o;      out[o][c] = in[o][c]
+//   kind 0: unit = 2048 elements (vec: 8 per thread, two 16-byte loads and one 16-byte
+//           store; else one output row o, out[o][c] = in[o][c])
 //   kind 1: unit = 8 rows c0 .. c0+7; out[c][o] = in[o][c] (0 for c >= cin), thread o
 //   kind 2: unit = output channel o;  out[o][t][c] = in[o][c][t], thread c
-//   kind 3: unit = input channel c;   out[c][t][o] = in[o][c][8 - t], thread o
+//   kind 3: unit = input channels c0 .. c0+3; out[c][t][o] = in[o][c][8 - t], thread o
 template <typename T>
 __global__ void __launch_bounds__(256) prepare_weights_kernel(const __grid_constant__ PrepArgs a) {
   int j = 0;
@@ -848,15 +899,30 @@ __global__ void __launch_bounds__(256) prepare_weights_kernel(const __grid_const
   const int t0 = threadIdx.x;
   switch (a.kind[j]) {
     case 0:
-      for (int c = t0; c < cin; c += 256)
-        out[static_cast<size_t>(u) * cin + c] = bw_from_f<T>(in[static_cast<size_t>(u) * cin + c]);
+      if (a.vec[j]) {
+        const size_t e = (static_cast<size_t>(u) * 256 + t0) * 8;
+        const float4 lo = __ldg(reinterpret_cast<const float4*>(in + e));
+        const float4 hi = __ldg(reinterpret_cast<const float4*>(in + e) + 1);
+        const float f[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+        *reinterpret_cast<uint4*>(out + e) = Vec16<T>::pack(f);
+      } else {
+        for (int c = t0; c < cin; c += 256)
+          out[static_cast<size_t>(u) * cin + c] = bw_from_f<T>(in[static_cast<size_t>(u) * cin + c]);
+      }
       break;
     case 1: {
       const int c0 = u * 8;
       float v[8];
+      if (a.vec[j] && c0 + 8 <= cin) {
+        const float4 lo = __ldg(reinterpret_cast<const float4*>(in + static_cast<size_t>(t0) * cin + c0));
+        const float4 hi = __ldg(reinterpret_cast<const float4*>(in + static_cast<size_t>(t0) * cin + c0) + 1);
+        v[0] = lo.x, v[1] = lo.y, v[2] = lo.z, v[3] = lo.w;
+        v[4] = hi.x, v[5] = hi.y, v[6] = hi.z, v[7] = hi.w;
+      } else {
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        v[i] = c0 + i < cin ? in[static_cast<size_t>(t0) * cin + c0 + i] : 0.f;
+        for (int i = 0; i < 8; ++i)
+          v[i] = c0 + i < cin ? in[static_cast<size_t>(t0) * cin + c0 + i] : 0.f;
+      }
 #pragma unroll
       for (int i = 0; i < 8; ++i) out[static_cast<size_t>(c0 + i) * 256 + t0] = bw_from_f<T>(v[i]);
       break;
@@ -871,12 +937,26 @@ __global__ void __launch_bounds__(256) prepare_weights_kernel(const __grid_const
       break;
     }
     default: {
-      const float* src = in + (static_cast<size_t>(t0) * 256 + u) * 9;
-      float v[9];
+      // four input channels c0 .. c0+3: thread o reads its contiguous 36 words in[o][c0..][..]
+      // (nine 16-byte loads when vec), every warp store covers 32 consecutive o
+      const int c0 = u * 4;
+      const float* src = in + (static_cast<size_t>(t0) * 256 + c0) * 9;
+      float v[36];
+      if (a.vec[j]) {
 #pragma unroll
-      for (int t = 0; t < 9; ++t) v[t] = src[8 - t];
+        for (int i = 0; i < 9; ++i) {
+          const float4 q = __ldg(reinterpret_cast<const float4*>(src) + i);
+          v[4 * i] = q.x, v[4 * i + 1] = q.y, v[4 * i + 2] = q.z, v[4 * i + 3] = q.w;
+        }
+      } else {
 #pragma unroll
-      for (int t = 0; t < 9; ++t) out[(static_cast<size_t>(u) * 9 + t) * 256 + t0] = bw_from_f<T>(v[t]);
+        for (int i = 0; i < 36; ++i) v[i] = src[i];
+      }
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc)
+#pragma unroll
+        for (int t = 0; t < 9; ++t)
+          out[(static_cast<size_t>(c0 + cc) * 9 + t) * 256 + t0] = bw_from_f<T>(v[cc * 9 + 8 - t]);
       break;
     }
   }
@@ -1004,10 +1084,12 @@ cudaError_t launch_dw_gemm(DType dt, const void* grad_out, const void* x, int N,
                      static_cast<const float*>(workspace), grad_w, a.ksplit, Cin,
                      static_cast<const float*>(a.db_partial), grad_b, a.ksplit * taps);
   }
-  const long long per = static_cast<long long>(taps) * 256 * Cin + (grad_b ? 256 : 0);
-  return launch_ex(reduce_partials_kernel, dim3(grid_for(per, 256)), dim3(256), 0, s, LaunchOpts(),
-                   1, static_cast<const float*>(workspace), grad_w, a.ksplit, taps, Cin,
-                   static_cast<const float*>(a.db_partial), grad_b, a.ksplit * taps);
+  // one block per 64 vectors of four outputs + one for the bias
+  const long long vblocks = (64LL * Cin + 63) / 64;
+  return launch_ex(reduce_partials_kernel, dim3(static_cast<unsigned>(vblocks + (grad_b ? 1 : 0))),
+                   dim3(256), 0, s, LaunchOpts(), 1, static_cast<const float*>(workspace), grad_w,
+                   a.ksplit, Cin, static_cast<const float*>(a.db_partial), grad_b,
+                   a.ksplit * taps);
 }
 
 // Column sums: at most 4 blocks per SM (all resident at once), each over a contiguous run of at
@@ -1080,7 +1162,14 @@ cudaError_t launch_prepare_weights(DType dt, const WeightPrepJob* jobs, int num_
     a.out[j] = jb.out;
     a.kind[j] = jb.kind;
     a.cin[j] = jb.cin;
-    blocks += jb.kind == 1 ? (jb.cin + 255) / 256 * 32 : 256;  // kind 1: 8-row units
+    // kind 0 vectorised: 2048-element units (256 * cin a multiple of 2048); kind 1: 8-row units
+    // (kind 3: 4-channel units, 64 per job)
+    a.vec[j] = aligned16(jb.in) && (jb.kind >= 2 || jb.cin % 8 == 0) &&
+               (jb.kind != 0 || aligned16(jb.out));
+    blocks += jb.kind == 1                 ? (jb.cin + 255) / 256 * 32
+              : jb.kind == 0 && a.vec[j] ? jb.cin / 8
+              : jb.kind == 3             ? 64
+                                         : 256;
   }
   a.first_block[num_jobs] = blocks;
   a.num_jobs = num_jobs;

@@ -589,6 +589,7 @@ struct SideStreams {
   cudaStream_t grads[4] = {};  // backward: P2..P5, least priority
   cudaEvent_t fork = nullptr, step = nullptr;
   cudaEvent_t join[8] = {};
+  cudaEvent_t mark[4] = {};  // backward: dM_l final
   bool ready = false;
   std::mutex mu;
 };
@@ -615,6 +616,8 @@ SideStreams* side_streams() {
     ok = ok && cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming) == cudaSuccess;
     ok = ok && cudaEventCreateWithFlags(&ss.step, cudaEventDisableTiming) == cudaSuccess;
     for (auto& e : ss.join)
+      ok = ok && cudaEventCreateWithFlags(&e, cudaEventDisableTiming) == cudaSuccess;
+    for (auto& e : ss.mark)
       ok = ok && cudaEventCreateWithFlags(&e, cudaEventDisableTiming) == cudaSuccess;
     cudaThreadExchangeStreamCaptureMode(&mode);
     if (!ok) {
@@ -661,6 +664,15 @@ class StreamFork {
     if (a == b) return cudaSuccess;
     cudaError_t e = cudaEventRecord(ss_->step, a);
     return e == cudaSuccess ? cudaStreamWaitEvent(b, ss_->step, 0) : e;
+  }
+  // Named points (i = 0..3, one record each per fork): `mark` records the work enqueued on
+  // stream a so far, `after` makes stream b wait for that record, however much later it is
+  // enqueued.
+  cudaError_t mark(int i, cudaStream_t a) const {
+    return forked_ ? cudaEventRecord(ss_->mark[i], a) : cudaSuccess;
+  }
+  cudaError_t after(int i, cudaStream_t b) const {
+    return forked_ ? cudaStreamWaitEvent(b, ss_->mark[i], 0) : cudaSuccess;
   }
 
  private:
@@ -965,9 +977,11 @@ int ufpn_neck_train_backward(int dtype, int N, const int* cin, const int* H, con
   }
   // Level l's chain stream: the 3x3 input gradient dM_l, then -- once the level below's dM
   // is final -- the top-down adjoint dM_l += up^T(dM_{l-1}), then the lateral input gradient
-  // dC_l.  Level l's weight-gradient stream: the 3x3's weight and bias gradients (from the
-  // start), then the lateral's once dM_l is final.  Every adjoint is enqueued before any
-  // lateral, so that each wait covers exactly the input gradient and adjoint before it.
+  // dC_l.  Level l's weight-gradient stream: the 3x3's weight and bias gradients, then the
+  // lateral's once dM_l is final.  Enqueued level by level (P5 first) with each level's 3x3
+  // weight gradient right after its input gradient: when the host issues about as fast as the
+  // GPU runs, the weight gradients -- half of the backward's work -- then start early instead
+  // of forming the step's tail (measured 1-2 % faster than enqueueing every chain first).
   StreamFork fork(s, true);
   for (int l = 3; l >= 0; --l) {
     rc = conv3x3_backward(dtype, nullptr, nullptr, flipped[l], dp[l], dm[l], nullptr, nullptr, N,
@@ -977,16 +991,16 @@ int ufpn_neck_train_backward(int dtype, int N, const int* cin, const int* H, con
                           grad_conv_b[l], N, H[l], W[l], fork.grads(l));
     if (rc != UFPN_OK) return rc;
   }
+  if ((e = fork.mark(0, fork.level(0))) != cudaSuccess) return cuda_fail(e, "level fork");
   for (int l = 1; l < 4; ++l) {
-    if ((e = fork.order(fork.level(l - 1), fork.level(l))) != cudaSuccess)
-      return cuda_fail(e, "level fork");
-    rc = ufpn_upsample_add_backward(dtype, dm[l - 1], dm[l], dm[l], N, 256, H[l], W[l], H[l - 1],
-                                    W[l - 1], fork.level(l));
+    if ((e = fork.after(l - 1, fork.level(l))) != cudaSuccess) return cuda_fail(e, "level fork");
+    rc = ufpn_upsample_add_backward(dtype, dm[l - 1], dm[l], dm[l], N, 256, H[l], W[l],
+                                    H[l - 1], W[l - 1], fork.level(l));
     if (rc != UFPN_OK) return rc;
+    if ((e = fork.mark(l, fork.level(l))) != cudaSuccess) return cuda_fail(e, "level fork");
   }
   for (int l = 3; l >= 0; --l) {
-    if ((e = fork.order(fork.level(l), fork.grads(l))) != cudaSuccess)
-      return cuda_fail(e, "level fork");
+    if ((e = fork.after(l, fork.grads(l))) != cudaSuccess) return cuda_fail(e, "level fork");
     rc = lateral_backward(dtype, x[l], nullptr, nullptr, dm[l], nullptr, grad_lat_w[l],
                           grad_lat_b[l], N, cin[l], H[l], W[l], fork.grads(l));
     if (rc != UFPN_OK) return rc;

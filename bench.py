@@ -479,7 +479,7 @@ def run_train(args, rank, world, local, dev):
         k = i % n_sets
         for p in neck.parameters():
             p.grad = None
-        for f in feats[k]:
+        for f in feats[k] + (static or []):
             f.grad = None
         if static is not None:
             with torch.no_grad():
