@@ -123,10 +123,10 @@ def time_steps(fn, steps, warmup=3, stream=None):
     return e0.elapsed_time(e1) / steps
 
 
-def cupti_timeline(fwd, n=14, skip=3):
+def cupti_timeline(fwd, n=14, skip=3, gap_us=15.0):
     """Per-kernel device timeline of the concurrent schedule: torch.profiler (CUPTI) over n
-    forwards, each followed by a synchronize so that forwards separate by an idle gap; the
-    first `skip` are dropped.  Per kernel (in start order within a forward): median start,
+    forwards, each followed by a synchronize so that forwards separate by an idle gap (one of
+    more than gap_us starts a new forward); the first `skip` are dropped.  Per kernel (in start order within a forward): median start,
     end and duration in us from the forward's first kernel start, and the median forward
     span.  None if the profiler is unavailable (for instance CUPTI held by another tool)."""
     import statistics
@@ -146,8 +146,8 @@ def cupti_timeline(fwd, n=14, skip=3):
         return None
     ev.sort(key=lambda e: e["ts"])
     fwds, end = [], None
-    for e in ev:  # a gap of > 15 us with no kernel running separates forwards
-        if end is None or e["ts"] > end + 15.0:
+    for e in ev:  # a gap of > gap_us with no kernel running separates forwards
+        if end is None or e["ts"] > end + gap_us:
             fwds.append([])
         fwds[-1].append(e)
         end = max(end or 0.0, e["ts"] + e["dur"])
@@ -514,6 +514,15 @@ def run_train(args, rank, world, local, dev):
     clk = clocks.stop()
     ms, images = job_throughput(e0.elapsed_time(e1), B * args.steps, world, dev)
     ms_per_step = ms / args.steps
+    kernel_timeline = None
+    if rank == 0 and world == 1 and not args.no_roofline:
+        def spaced(i):  # (steps apart by > 1 ms of idle GPU; the forward-backward gap is less)
+            step(i)
+            time.sleep(0.003)
+        kernel_timeline = cupti_timeline(spaced, gap_us=1000.0)
+        if kernel_timeline is not None:
+            kernel_timeline["step_us"] = kernel_timeline.pop("forward_us")
+            kernel_timeline["steps"] = kernel_timeline.pop("forwards")
     peaks = measured_peaks()
     flops = 3.0 * neck_flops(B, R50_CHANNELS, sizes)  # forward + input and weight gradients
     achieved = flops / (ms_per_step * 1e-3) / 1e12
@@ -540,6 +549,8 @@ def run_train(args, rank, world, local, dev):
                          "traffic": None},
             "device_status": U.device_status(),
         }
+        if kernel_timeline is not None:
+            line["kernel_timeline"] = kernel_timeline
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
