@@ -104,3 +104,25 @@ def test_package_exports_reference_api():
     for name in ("UnifiedFPN", "fpn_lateral_conv", "fpn_upsample_bilinear", "fpn_forward_pytorch",
                  "benchmark_fpn", "profile_fpn", "get_device_info", "check_installation"):
         assert hasattr(unified_fpn, name)
+
+
+def test_training_workspace_layout_and_pointer_arrays():
+    """Host side of the training path: the forward's one workspace holds the 16 weight layouts
+    and the four merged maps 256-byte aligned, in order and without overlap; the driver calls'
+    int and pointer arrays sit at the addresses handed to the library."""
+    from unified_fpn import training as T
+    cin, H, W, N = [256, 512, 1024, 2048], [200, 100, 50, 25], [304, 152, 76, 38], 2
+    offs, total = T._workspace_layout(N, cin, H, W, 2)
+    sizes = []
+    for c in cin:
+        sizes += [256 * c, (c + 255) // 256 * 256 * 256, 256 * 9 * 256, 256 * 9 * 256]
+    sizes += [N * h * w * 256 for h, w in zip(H, W)]
+    assert len(offs) == 20 and offs[0] == 0
+    assert all(o % 256 == 0 for o in offs)
+    ends = [o + 2 * n for o, n in zip(offs, sizes)]
+    assert all(e <= o for e, o in zip(ends, offs[1:])) and ends[-1] <= total
+    assert total - ends[-1] < 256
+    ints, ptrs = [3, 1, 4, 1, 5, 9], [0x1000, None, 0x3000]
+    ia, pa, ip, pp = T._arrays(ints, ptrs)
+    assert [ctypes.c_int.from_address(ip(k)).value for k in range(len(ints))] == ints
+    assert [ctypes.c_void_p.from_address(pp(k)).value for k in range(len(ptrs))] == ptrs

@@ -293,3 +293,45 @@ def test_training_step_full_size_properties(cuda_device):
     c = step(run)
     assert all(torch.equal(x, y) for x, y in zip(a, c))
     assert U.device_status() == 0
+
+
+def test_interleaved_steps_and_gradient_accumulation(cuda_device):
+    """Each forward keeps its own workspace (merged maps, weight layouts) and the fp32 weight
+    gradients are views of one buffer per backward: two forwards followed by their backwards in
+    reverse order give bitwise the gradients of two separate steps, and accumulating both into
+    .grad (no reset in between) gives their sum."""
+    import unified_fpn as U
+    dev = torch.device(cuda_device)
+    sizes = O.level_sizes(96, 128)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(91)
+    sets = [[_cl(torch.randn(2, c, h, w, device=dev, generator=gen).to(torch.bfloat16)).requires_grad_()
+             for c, (h, w) in zip(O.R50_CHANNELS, sizes)] for _ in range(2)]
+    osz = list(sizes) + [((sizes[3][0] - 1) // 2 + 1, (sizes[3][1] - 1) // 2 + 1)]
+    grads = [[_cl(torch.randn(2, 256, h, w, device=dev, generator=gen).to(torch.bfloat16)) for h, w in osz]
+             for _ in range(2)]
+    neck = U.FPNNeck(O.R50_CHANNELS).to(dev)
+
+    def reset():
+        for p in neck.parameters():
+            p.grad = None
+        for s in sets:
+            for f in s:
+                f.grad = None
+
+    alone = []
+    for k in range(2):
+        reset()
+        torch.autograd.backward(neck(sets[k]), grads[k])
+        alone.append([p.grad.clone() for p in neck.parameters()] + [f.grad.clone() for f in sets[k]])
+    reset()
+    outs = [neck(sets[0]), neck(sets[1])]
+    torch.autograd.backward(outs[1], grads[1])
+    second = [p.grad.clone() for p in neck.parameters()] + [f.grad.clone() for f in sets[1]]
+    torch.autograd.backward(outs[0], grads[0])  # accumulates into the parameters' .grad
+    torch.cuda.synchronize()
+    assert all(torch.equal(x, y) for x, y in zip(second, alone[1]))
+    assert all(torch.equal(f.grad, y) for f, y in zip(sets[0], alone[0][16:]))
+    for p, a0, a1 in zip(neck.parameters(), alone[0][:16], alone[1][:16]):
+        assert torch.equal(p.grad, a1 + a0)
+    assert U.device_status() == 0
