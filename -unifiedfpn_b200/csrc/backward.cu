@@ -399,40 +399,85 @@ __global__ void __launch_bounds__(256) reduce_partials_kernel(const float* __res
   }
 }
 
-// 3x3 weight gradient in [256 o][Cin c][9 t] order: block (o, c0) sums partial[s][t][o][c0 ..
-// c0 + 31] for its 9 x 32 outputs -- thread (t, vector, lane): four lanes per 16-byte vector,
-// fixed_order_sum4 -- stages them as [cc][t] and writes the 288 contiguous outputs in order.
-// The last block (with grad_b) sums the bias partials.  Cin a multiple of 4.
+// 3x3 weight gradient in [256 o][Cin c][9 t] order.  Block (o, 256-channel chunk) sums
+// partial[s][t][o][chunk] for its 9 x 256 outputs: 576 items of (t, 16-byte vector of four
+// channels), two per thread, each summed by its thread over s as four chains s = k, k + 4, ..
+// added as (c0 + c1) + (c2 + c3) -- fixed_order_sum's association per element, so the sums are
+// bitwise fixed_order_sum's -- with eight 16-byte loads in flight per thread; every warp reads
+// 512 contiguous bytes of one (s, t) row.  The block stages its outputs as [c][t] and writes
+// its 2304 contiguous outputs in order.  The last block (with grad_b) sums the bias partials.
+// Cin a multiple of 4.
+constexpr int kTaps9Chunk = 256;
 __global__ void __launch_bounds__(288) reduce_partials_taps9_kernel(
     const float* __restrict__ partial, float* __restrict__ out, int ksplit, int Cin,
     const float* __restrict__ db_partial, float* __restrict__ grad_b, int db_rows) {
-  __shared__ float tile[32 * 9];
-  const int cblocks = (Cin + 31) / 32;
-  if (static_cast<int>(blockIdx.x) == 256 * cblocks) {  // bias
+  __shared__ float tile[kTaps9Chunk * 9];
+  const int chunks = (Cin + kTaps9Chunk - 1) / kTaps9Chunk;
+  if (static_cast<int>(blockIdx.x) == 256 * chunks) {  // bias
     const int o = threadIdx.x;
     if (o < 256)
       grad_b[o] = fixed_order_sum(db_rows, [&](int r) { return __ldg(db_partial + r * 256 + o); });
     return;
   }
-  const int o = static_cast<int>(blockIdx.x) / cblocks;
-  const int c0 = (static_cast<int>(blockIdx.x) % cblocks) * 32;
-  const int t = threadIdx.x / 32, cv = (threadIdx.x % 32) / 4;
+  const int o = static_cast<int>(blockIdx.x) / chunks;
+  const int c0 = (static_cast<int>(blockIdx.x) % chunks) * kTaps9Chunk;
   const long long per = 9LL * 256 * Cin;
-  // (every lane takes part in the group's shuffles; a vector past Cin sums nothing)
-  const bool in = c0 + cv * 4 < Cin;
-  const size_t idx = in ? (static_cast<size_t>(t) * 256 + o) * Cin + c0 + cv * 4 : 0;
-  const float4 r = fixed_order_sum4(partial + idx, per, in ? ksplit : 0);
-  {
-    if (in && (threadIdx.x & 3) == 0) {
-      tile[(cv * 4 + 0) * 9 + t] = r.x;
-      tile[(cv * 4 + 1) * 9 + t] = r.y;
-      tile[(cv * 4 + 2) * 9 + t] = r.z;
-      tile[(cv * 4 + 3) * 9 + t] = r.w;
+  const float* src[2];
+  bool in[2];
+  int t_of[2], v_of[2];
+#pragma unroll
+  for (int it = 0; it < 2; ++it) {
+    const int item = static_cast<int>(threadIdx.x) + it * 288;  // 0 .. 575
+    t_of[it] = item / (kTaps9Chunk / 4);
+    v_of[it] = item % (kTaps9Chunk / 4);
+    in[it] = c0 + v_of[it] * 4 < Cin;
+    src[it] = partial + (static_cast<size_t>(t_of[it]) * 256 + o) * Cin + c0 + v_of[it] * 4;
+  }
+  float4 acc[2][4];
+#pragma unroll
+  for (int it = 0; it < 2; ++it)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc[it][k] = make_float4(0.f, 0.f, 0.f, 0.f);
+  auto add = [](float4& a, const float4 t) {
+    a.x += t.x;
+    a.y += t.y;
+    a.z += t.z;
+    a.w += t.w;
+  };
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  int s = 0;
+  for (; s + 4 <= ksplit; s += 4) {
+    float4 t[2][4];
+#pragma unroll
+    for (int it = 0; it < 2; ++it)
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        t[it][k] = in[it] ? __ldg(reinterpret_cast<const float4*>(src[it] + (s + k) * per)) : zero;
+#pragma unroll
+    for (int it = 0; it < 2; ++it)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) add(acc[it][k], t[it][k]);
+  }
+#pragma unroll
+  for (int k = 0; k < 3; ++k)  // the tail: s + k < ksplit goes to chain k
+    if (s + k < ksplit) {
+#pragma unroll
+      for (int it = 0; it < 2; ++it)
+        if (in[it]) add(acc[it][k], __ldg(reinterpret_cast<const float4*>(src[it] + (s + k) * per)));
     }
+#pragma unroll
+  for (int it = 0; it < 2; ++it) {
+    if (!in[it]) continue;
+    const float4 a = acc[it][0], b = acc[it][1], c = acc[it][2], d = acc[it][3];
+    const float r[4] = {(a.x + b.x) + (c.x + d.x), (a.y + b.y) + (c.y + d.y),
+                        (a.z + b.z) + (c.z + d.z), (a.w + b.w) + (c.w + d.w)};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) tile[(v_of[it] * 4 + j) * 9 + t_of[it]] = r[j];
   }
   __syncthreads();
-  const int j = threadIdx.x;  // output element c0 * 9 + j of row o
-  if (c0 + j / 9 < Cin) out[(static_cast<size_t>(o) * Cin + c0) * 9 + j] = tile[j];
+  const int n_out = (Cin - c0 < kTaps9Chunk ? Cin - c0 : kTaps9Chunk) * 9;
+  float* dst = out + (static_cast<size_t>(o) * Cin + c0) * 9;
+  for (int j = threadIdx.x; j < n_out; j += 288) dst[j] = tile[j];
 }
 
 // ------------------------------------------------------------------ bias gradient
@@ -1078,8 +1123,8 @@ cudaError_t launch_dw_gemm(DType dt, const void* grad_out, const void* x, int N,
                 map_p, a);
   if (e != cudaSuccess) return e;
   if (taps == 9) {
-    // one block per (output channel, 32 input channels) + one for the bias
-    const unsigned grid9 = static_cast<unsigned>(256 * ((Cin + 31) / 32) + (grad_b ? 1 : 0));
+    // one block per (output channel, 256 input channels) + one for the bias
+    const unsigned grid9 = static_cast<unsigned>(256 * ((Cin + 255) / 256) + (grad_b ? 1 : 0));
     return launch_ex(reduce_partials_taps9_kernel, dim3(grid9), dim3(288), 0, s, LaunchOpts(), 1,
                      static_cast<const float*>(workspace), grad_w, a.ksplit, Cin,
                      static_cast<const float*>(a.db_partial), grad_b, a.ksplit * taps);
