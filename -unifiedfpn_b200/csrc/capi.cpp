@@ -706,10 +706,12 @@ const float* device_zeros() {
 }
 
 // Lateral backward; the input gradient uses w_t ([cblk * 256][256], w transposed with zero
-// rows beyond Cin) if given, else transposes w into scratch.
+// rows beyond Cin) if given, else transposes w into scratch.  ws: the caller's scratch (256-
+// byte aligned, at least the call's need: a weight gradient's dw_gemm_workspace_bytes), or
+// null to allocate on the stream what the call needs (nothing for an input gradient with w_t).
 int lateral_backward(int dtype, const void* x, const void* w, const void* w_t,
                      const void* grad_out, void* grad_x, float* grad_w, float* grad_b, int N,
-                     int Cin, int H, int W, void* stream) {
+                     int Cin, int H, int W, void* stream, void* ws = nullptr) {
   DType dt;
   if (!parse_16bit(dtype, &dt)) return fail(UFPN_ERR_UNSUPPORTED, "backward takes bf16 or fp16");
   if (!grad_out || (grad_x && !w && !w_t) || (grad_w && !x))
@@ -728,9 +730,13 @@ int lateral_backward(int dtype, const void* x, const void* w, const void* w_t,
   // (the bias gradient comes out of the weight-gradient launch when both are asked for)
   const size_t cs_bytes = grad_b && !grad_w ? ufpn::colsum_workspace_bytes(pixels, 256) : 0;
   StreamScratch scratch(s);
-  cudaError_t e = scratch.alloc(wt_bytes + dw_bytes + cs_bytes + 16);
-  if (e != cudaSuccess) return cuda_fail(e, "backward scratch");
-  uint8_t* base = static_cast<uint8_t*>(scratch.p);
+  cudaError_t e = cudaSuccess;
+  uint8_t* base = static_cast<uint8_t*>(ws);
+  if (!base && wt_bytes + dw_bytes + cs_bytes > 0) {
+    if ((e = scratch.alloc(wt_bytes + dw_bytes + cs_bytes)) != cudaSuccess)
+      return cuda_fail(e, "backward scratch");
+    base = static_cast<uint8_t*>(scratch.p);
+  }
   if (grad_x) {
     const float* zero_bias = device_zeros();
     if (!zero_bias) return fail(UFPN_ERR_CUDA, "device zeros");
@@ -764,10 +770,10 @@ int lateral_backward(int dtype, const void* x, const void* w, const void* w_t,
 }
 
 // 3x3 backward; the input gradient uses w_f ([256 c][9][256 o], the packed weights flipped)
-// if given, else flips w into scratch.
+// if given, else flips w into scratch.  ws: as for lateral_backward.
 int conv3x3_backward(int dtype, const void* x, const void* w, const void* w_f,
                      const void* grad_out, void* grad_x, float* grad_w, float* grad_b, int N,
-                     int H, int W, void* stream) {
+                     int H, int W, void* stream, void* ws = nullptr) {
   DType dt;
   if (!parse_16bit(dtype, &dt)) return fail(UFPN_ERR_UNSUPPORTED, "backward takes bf16 or fp16");
   if (!grad_out || (grad_x && !w && !w_f) || (grad_w && !x))
@@ -784,9 +790,13 @@ int conv3x3_backward(int dtype, const void* x, const void* w, const void* w_f,
   // (the bias gradient comes out of the weight-gradient launch when both are asked for)
   const size_t cs_bytes = grad_b && !grad_w ? ufpn::colsum_workspace_bytes(pixels, 256) : 0;
   StreamScratch scratch(s);
-  cudaError_t e = scratch.alloc(wf_bytes + dw_bytes + cs_bytes + 16);
-  if (e != cudaSuccess) return cuda_fail(e, "backward scratch");
-  uint8_t* base = static_cast<uint8_t*>(scratch.p);
+  cudaError_t e = cudaSuccess;
+  uint8_t* base = static_cast<uint8_t*>(ws);
+  if (!base && wf_bytes + dw_bytes + cs_bytes > 0) {
+    if ((e = scratch.alloc(wf_bytes + dw_bytes + cs_bytes)) != cudaSuccess)
+      return cuda_fail(e, "backward scratch");
+    base = static_cast<uint8_t*>(scratch.p);
+  }
   if (grad_x) {
     const float* zero_bias = device_zeros();
     if (!zero_bias) return fail(UFPN_ERR_CUDA, "device zeros");
@@ -954,8 +964,19 @@ int ufpn_neck_train_backward(int dtype, int N, const int* cin, const int* H, con
   for (int l = 0; l < 4; ++l)
     if (!grad_out[l] && map_bytes[l] > zero_bytes) zero_bytes = map_bytes[l];
   const size_t dp5_bytes = grad_p6 ? map_bytes[3] : 0;
+  // then the eight weight gradients' split-K workspaces (they run concurrently on the level
+  // streams, each in its own region; one allocation instead of one per launch)
+  auto r256 = [](size_t b) { return (b + 255) / 256 * 256; };
+  size_t ws3[4], wsl[4], ws_bytes = 0;
+  const size_t ws_base = off[4] + zero_bytes + dp5_bytes;
+  for (int l = 0; l < 4; ++l) {
+    ws3[l] = ws_base + ws_bytes;
+    ws_bytes += r256(ufpn::dw_gemm_workspace_bytes(N, H[l], W[l], 256, 9));
+    wsl[l] = ws_base + ws_bytes;
+    ws_bytes += r256(ufpn::dw_gemm_workspace_bytes(N, H[l], W[l], cin[l], 1));
+  }
   StreamScratch scratch(s);
-  cudaError_t e = scratch.alloc(off[4] + zero_bytes + dp5_bytes + 16);
+  cudaError_t e = scratch.alloc(ws_base + ws_bytes + 16);
   if (e != cudaSuccess) return cuda_fail(e, "train backward scratch");
   uint8_t* base = static_cast<uint8_t*>(scratch.p);
   void* dm[4];
@@ -988,7 +1009,7 @@ int ufpn_neck_train_backward(int dtype, int N, const int* cin, const int* H, con
                           H[l], W[l], fork.level(l));
     if (rc != UFPN_OK) return rc;
     rc = conv3x3_backward(dtype, merged[l], nullptr, nullptr, dp[l], nullptr, grad_conv_w[l],
-                          grad_conv_b[l], N, H[l], W[l], fork.grads(l));
+                          grad_conv_b[l], N, H[l], W[l], fork.grads(l), base + ws3[l]);
     if (rc != UFPN_OK) return rc;
   }
   if ((e = fork.mark(0, fork.level(0))) != cudaSuccess) return cuda_fail(e, "level fork");
@@ -1002,7 +1023,7 @@ int ufpn_neck_train_backward(int dtype, int N, const int* cin, const int* H, con
   for (int l = 3; l >= 0; --l) {
     if ((e = fork.after(l, fork.grads(l))) != cudaSuccess) return cuda_fail(e, "level fork");
     rc = lateral_backward(dtype, x[l], nullptr, nullptr, dm[l], nullptr, grad_lat_w[l],
-                          grad_lat_b[l], N, cin[l], H[l], W[l], fork.grads(l));
+                          grad_lat_b[l], N, cin[l], H[l], W[l], fork.grads(l), base + wsl[l]);
     if (rc != UFPN_OK) return rc;
     if (grad_x) {
       rc = lateral_backward(dtype, nullptr, nullptr, lat16_t[l], dm[l], grad_x[l], nullptr,
