@@ -912,14 +912,57 @@ int ufpn_neck_train_forward(int dtype, int N, const int* cin, const int* H, cons
   if (rc != UFPN_OK) return rc;
   // Top-down on the caller's stream, M_l = lateral(C_l) + up(M_{l+1}); each level's 3x3 starts
   // on its own stream as soon as M_l is written (P5, P4, P3 on side streams beside the next
-  // laterals, P2 on the caller's).
-  StreamFork fork(static_cast<cudaStream_t>(stream), false);
+  // laterals, P2 on the caller's).  Where the maps upsample and the geometry fits its plan, as
+  // the forward engine does: the raw P5 / P4 / P3 laterals in one launch on CTA pairs (L5 =
+  // M5, L4 into scratch, L3 into M3's map), one launch for both merges (M4 = L4 + up(M5), M3 =
+  // L3 + up(M4) in place), then the P2 lateral with the top-down add -- instead of a chain of
+  // four laterals, each waiting for the one above.
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  StreamFork fork(s, false);
+  StreamScratch l4(s);
+  bool grouped = false;
+  if (H[3] <= H[2] && W[3] <= W[2] && H[2] <= H[1] && W[2] <= W[1]) {
+    ufpn::DType dt16;
+    parse_16bit(dtype, &dt16);
+    ufpn::NeckLevel lv[4] = {};
+    for (int l = 0; l < 4; ++l) {
+      lv[l].x = x[l];
+      lv[l].lat_w = lat16[l];
+      lv[l].lat_b = lat_b[l];
+      lv[l].merged = merged[l];
+      lv[l].Cin = cin[l];
+      lv[l].H = H[l];
+      lv[l].W = W[l];
+      lv[l].lat_tiling = ufpn::default_tiling(H[l], W[l]);
+    }
+    cudaError_t e = l4.alloc(static_cast<size_t>(N) * H[2] * W[2] * 256 * ufpn::dtype_size(dt16));
+    if (e != cudaSuccess) return cuda_fail(e, "train forward scratch");
+    lv[2].merged = l4.p;
+    ufpn::LateralGroupPlan lplan;
+    const int which[3] = {3, 2, 1};
+    e = ufpn::plan_lateral_group_pair(lplan, dt16, N, lv, which, 3, device_status_word(), 0);
+    if (e == cudaSuccess) {
+      grouped = true;
+      if ((e = ufpn::launch_lateral_group_pair(lplan, s)) != cudaSuccess)
+        return cuda_fail(e, "grouped laterals");
+      // (the P5 3x3 needs M5 = L5 only: its stream waits for the grouped launch, not the merge)
+      if ((e = fork.order(s, fork.level(3))) != cudaSuccess) return cuda_fail(e, "level fork");
+      if ((e = ufpn::launch_merge_two_levels(dt16, merged[3], l4.p, merged[2], merged[1],
+                                             merged[1], N, H[3], W[3], H[2], W[2], H[1], W[1],
+                                             s)) != cudaSuccess)
+        return cuda_fail(e, "merge P4 and P3");
+    } else if (e != cudaErrorNotSupported) {
+      return cuda_fail(e, "plan grouped laterals");
+    }
+  }
   for (int l = 3; l >= 0; --l) {
-    rc = ufpn_lateral_conv(dtype, UFPN_LAYOUT_NHWC, x[l], lat16[l], lat_b[l],
-                           l < 3 ? merged[l + 1] : nullptr, merged[l], N, cin[l], H[l], W[l], 256,
-                           l < 3 ? H[l + 1] : 0, l < 3 ? W[l + 1] : 0, stream);
-    if (rc != UFPN_OK) return rc;
-    cudaError_t e = fork.order(static_cast<cudaStream_t>(stream), fork.level(l));
+    if (!grouped || l == 0) {
+      rc = ufpn_lateral_conv(dtype, UFPN_LAYOUT_NHWC, x[l], lat16[l], lat_b[l],
+                             l < 3 ? merged[l + 1] : nullptr, merged[l], N, cin[l], H[l], W[l],
+                             256, l < 3 ? H[l + 1] : 0, l < 3 ? W[l + 1] : 0, stream);
+      if (rc != UFPN_OK) return rc;
+    }
+    cudaError_t e = grouped && l == 3 ? cudaSuccess : fork.order(s, fork.level(l));
     if (e != cudaSuccess) return cuda_fail(e, "level fork");
     // 3x3s on single-CTA halo tiles, with the mixed tiling or the transposed view where that
     // needs fewer tiles (not with the fused P6): 2-5 % faster per training step than CTA pairs

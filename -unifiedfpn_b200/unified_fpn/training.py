@@ -77,7 +77,9 @@ def fpn_neck_forward_train(feats: Sequence[torch.Tensor], lateral_w: Sequence[to
     channels_last, and the opaque state ``fpn_neck_backward`` needs (the inputs, and one
     workspace holding the merged maps M2..M5 and the prepared weight layouts).  One library
     call (``ufpn_neck_train_forward``): the weight layouts of the whole step in one launch, the
-    four laterals top-down, the four 3x3s (single-CTA halo tiles)."""
+    laterals top-down (the raw P5 / P4 / P3 laterals in one launch and both merges in another,
+    as the forward engine runs them, then the P2 lateral with the top-down add), the four 3x3s
+    (single-CTA halo tiles)."""
     if len(feats) != 4 or len(lateral_w) != 4 or len(output_w) != 4:
         raise ValueError("feats and weights must be C2..C5 / four levels")
     dt = feats[0].dtype
