@@ -335,3 +335,31 @@ def test_interleaved_steps_and_gradient_accumulation(cuda_device):
     for p, a0, a1 in zip(neck.parameters(), alone[0][:16], alone[1][:16]):
         assert torch.equal(p.grad, a1 + a0)
     assert U.device_status() == 0
+
+
+@pytest.mark.parametrize("h,w,batch", [(800, 1216, 2), (128, 160, 2), (640, 640, 4)])
+def test_training_forward_equals_the_inference_forward(cuda_device, h, w, batch):
+    """The training step's forward (FPNNeck: grouped raw laterals, both merges in one launch,
+    the P2 lateral with the top-down add, single-CTA halo 3x3s) gives bitwise the outputs of
+    UnifiedFPN's forward with the same fp32 weights: P2..P6."""
+    import unified_fpn as U
+    dev = torch.device(cuda_device)
+    sizes = O.level_sizes(h, w)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3)
+    feats = [_cl(torch.randn(batch, c, hh, ww, device=dev, generator=gen).clamp_min_(0).to(torch.bfloat16))
+             for c, (hh, ww) in zip(O.R50_CHANNELS, sizes)]
+    neck = U.FPNNeck(O.R50_CHANNELS).to(dev)
+    with torch.no_grad():
+        for b in list(neck.lateral_b) + list(neck.output_b):
+            b.normal_(0, 0.1, generator=gen)
+        outs = neck(feats)
+    fpn = U.UnifiedFPN(device=dev)
+    fpn.initialize_weights([p.detach() for p in neck.lateral_w], [p.detach() for p in neck.lateral_b],
+                           [p.detach() for p in neck.output_w], [p.detach() for p in neck.output_b])
+    ref = fpn(feats, return_p6=True)
+    torch.cuda.synchronize()
+    assert len(outs) == len(ref) == 5
+    for a, r in zip(outs, ref):
+        assert a.shape == r.shape and torch.equal(a, r)
+    assert U.device_status() == 0
