@@ -892,6 +892,62 @@ int ufpn_prepare_neck_weights(int dtype, int levels, const float* const* lat_w, 
   return e == cudaSuccess ? UFPN_OK : cuda_fail(e, "prepare weights");
 }
 
+namespace {
+// The grouped P5 / P4 / P3 lateral plan of the training forward, cached: planning costs the
+// host ~25 us and its result depends only on the key below (the lateral tilings follow from
+// H and W), which repeats from step to step as the caching allocators hand back the same
+// buffers.  A few entries, replaced round robin; a miss plans again.
+struct GroupPlanKey {
+  int dev, dtype, N, cin[3], H[3], W[3];
+  const void* x[3];
+  const void* w[3];
+  const float* b[3];
+  void* m[3];
+  int* status;
+};
+struct GroupPlanCache {
+  std::mutex mu;
+  GroupPlanKey key[4];
+  ufpn::LateralGroupPlan plan[4];
+  bool valid[4] = {};
+  int next = 0;
+};
+cudaError_t grouped_lateral_plan(ufpn::LateralGroupPlan& out, ufpn::DType dt, int N,
+                                 const ufpn::NeckLevel* lv, int* status) {
+  static GroupPlanCache cache;
+  GroupPlanKey k;
+  std::memset(&k, 0, sizeof(k));  // (padding too: keys compare as bytes)
+  if (cudaGetDevice(&k.dev) != cudaSuccess) k.dev = -1;
+  k.dtype = static_cast<int>(dt);
+  k.N = N;
+  for (int i = 0; i < 3; ++i) {
+    const ufpn::NeckLevel& l = lv[3 - i];
+    k.cin[i] = l.Cin, k.H[i] = l.H, k.W[i] = l.W;
+    k.x[i] = l.x, k.w[i] = l.lat_w, k.b[i] = l.lat_b, k.m[i] = l.merged;
+  }
+  k.status = status;
+  {
+    std::lock_guard<std::mutex> lk(cache.mu);
+    for (int i = 0; i < 4; ++i)
+      if (cache.valid[i] && std::memcmp(&cache.key[i], &k, sizeof(k)) == 0) {
+        out = cache.plan[i];
+        return cudaSuccess;
+      }
+  }
+  const int which[3] = {3, 2, 1};
+  const cudaError_t e = ufpn::plan_lateral_group_pair(out, dt, N, lv, which, 3, status, 0);
+  if (e == cudaSuccess) {
+    std::lock_guard<std::mutex> lk(cache.mu);
+    const int i = cache.next;
+    cache.next = (i + 1) % 4;
+    cache.key[i] = k;
+    cache.plan[i] = out;
+    cache.valid[i] = true;
+  }
+  return e;
+}
+}  // namespace
+
 int ufpn_neck_train_forward(int dtype, int N, const int* cin, const int* H, const int* W,
                             const void* const* x, const float* const* lat_w,
                             const float* const* lat_b, const float* const* conv_w,
@@ -939,8 +995,7 @@ int ufpn_neck_train_forward(int dtype, int N, const int* cin, const int* H, cons
     if (e != cudaSuccess) return cuda_fail(e, "train forward scratch");
     lv[2].merged = l4.p;
     ufpn::LateralGroupPlan lplan;
-    const int which[3] = {3, 2, 1};
-    e = ufpn::plan_lateral_group_pair(lplan, dt16, N, lv, which, 3, device_status_word(), 0);
+    e = grouped_lateral_plan(lplan, dt16, N, lv, device_status_word());
     if (e == cudaSuccess) {
       grouped = true;
       if ((e = ufpn::launch_lateral_group_pair(lplan, s)) != cudaSuccess)
