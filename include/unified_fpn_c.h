@@ -336,11 +336,16 @@ int ufpn_prepare_neck_weights(int dtype, int levels, const float* const* lat_w, 
  * Forward: prepares the weight layouts (lat16, lat16_t, packed, flipped: caller-allocated as
  * in ufpn_prepare_neck_weights; lat16_t / flipped may be NULL for inference), computes the
  * merged maps M2..M5 (merged[l], [N][H][W][256]) top-down and P2..P5 (out[l]) with P6 (p6, or
- * NULL) -- the forward of UnifiedFPN on the training kernels.
+ * NULL) -- bitwise the outputs of UnifiedFPN's forward with the same weights.
  * Backward: from dP2..dP5 (grad_out[l], 16-bit NHWC; NULL = zero) and dP6 (grad_p6 or NULL) and
  * the forward's x, merged, lat16_t and flipped, writes dC_l (grad_x[l]; grad_x or an entry
  * NULL skips it) and the fp32 gradients of every weight ([256][cin] lateral, [256][256][3][3]
- * 3x3) and bias; the scratch for dM2..dM5 is stream-ordered on `stream`. */
+ * 3x3) and bias, deterministically (fixed-order sums, no atomics).  Both calls spread their
+ * per-level work over the library's own side streams, which wait for `stream` on entry and
+ * are joined back into it before the call returns, so work enqueued on `stream` afterwards
+ * sees every result; their scratch (the backward's dM2..dM5 and split-K workspaces) is
+ * stream-ordered on `stream`.  One such call at a time per device (calls from several threads
+ * take turns). */
 int ufpn_neck_train_forward(int dtype, int N, const int* cin, const int* H, const int* W,
                             const void* const* x, const float* const* lat_w,
                             const float* const* lat_b, const float* const* conv_w,
